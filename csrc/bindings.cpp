@@ -1,0 +1,83 @@
+// Python bindings of the vllm_moet_b200 native library (_C).
+#include <torch/extension.h>
+
+// norm_quant.cu
+void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> add, c10::optional<torch::Tensor> x_out,
+                   torch::Tensor w, double eps, c10::optional<torch::Tensor> y_out,
+                   c10::optional<torch::Tensor> q0, c10::optional<torch::Tensor> s0,
+                   c10::optional<torch::Tensor> q1, c10::optional<torch::Tensor> s1, int64_t ostride);
+void swiglu_quant(torch::Tensor in, double limit, c10::optional<torch::Tensor> n_rows, int64_t layout,
+                  torch::Tensor q, torch::Tensor s);
+void quant_fp8(torch::Tensor x, int64_t layout, torch::Tensor q, torch::Tensor s);
+// gemv_fp8.cu
+void gemv_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tensor sw, torch::Tensor out,
+              c10::optional<torch::Tensor> resid);
+// moe_route.cu
+void router_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_t k, bool sigmoid,
+                 int64_t n_group, int64_t topk_group, bool norm, double scaling, torch::Tensor ids,
+                 torch::Tensor wts);
+void build_pairs(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor rank_scratch,
+                 torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
+                 torch::Tensor status);
+// moe_w2.cu
+void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor> gather, torch::Tensor pairs,
+                 torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
+                 torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
+                 c10::optional<torch::Tensor> miss_count);
+void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::optional<torch::Tensor> resid,
+                 c10::optional<torch::Tensor> shared_out, c10::optional<torch::Tensor> out,
+                 c10::optional<torch::Tensor> out_f32);
+
+// mla_decode.cu
+void mla_decode(torch::Tensor q, torch::Tensor kv, torch::Tensor block_table, torch::Tensor seq_of_tok,
+                torch::Tensor pos_of_tok, torch::Tensor o_part, torch::Tensor ml_part, double scale,
+                torch::Tensor status);
+void mla_combine(torch::Tensor o_part, torch::Tensor ml_part, c10::optional<torch::Tensor> out,
+                 c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> qs);
+// mla_prep.cu
+void q_prep(torch::Tensor qb, int64_t Hh, int64_t nope, int64_t rope, torch::Tensor pos_of_tok,
+            torch::Tensor cos_sin, c10::optional<torch::Tensor> qn_q, c10::optional<torch::Tensor> qn_s,
+            c10::optional<torch::Tensor> qcat, int64_t rope_off, c10::optional<torch::Tensor> q_out);
+void kv_prep(torch::Tensor kva, int64_t lat, int64_t rope, torch::Tensor norm_w, double eps, torch::Tensor pos_of_tok,
+             torch::Tensor cos_sin, c10::optional<torch::Tensor> slot_mapping, int64_t cache_mode,
+             c10::optional<torch::Tensor> cache, c10::optional<torch::Tensor> lat_out,
+             c10::optional<torch::Tensor> rope_out, c10::optional<torch::Tensor> lat_q,
+             c10::optional<torch::Tensor> lat_s, torch::Tensor status);
+// mla_prefill.cu
+void mla_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kr, torch::Tensor cu_seqlens, int64_t max_len,
+                 double scale, c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_s,
+                 c10::optional<torch::Tensor> out_bf16);
+// quant_pack.cu
+void nvfp4_quant(torch::Tensor w, double ts, torch::Tensor packed, torch::Tensor sf);
+void w2_quant_pack(torch::Tensor packed, torch::Tensor sf, double ts, int64_t zero_mode, torch::Tensor codes_plane,
+                   torch::Tensor scale_plane, c10::optional<torch::Tensor> fp4_plane,
+                   c10::optional<torch::Tensor> counters);
+// sampling.cu
+void argmax_lse(torch::Tensor logits, torch::Tensor ids, c10::optional<torch::Tensor> lse,
+                c10::optional<torch::Tensor> maxv);
+void mtp_accept(torch::Tensor targets, torch::Tensor tokens, torch::Tensor out_tokens, torch::Tensor n_acc,
+                c10::optional<torch::Tensor> active);
+void mtp_finalize(torch::Tensor targets, torch::Tensor n_acc, torch::Tensor drafts, torch::Tensor tokens,
+                  torch::Tensor seq_pos, c10::optional<torch::Tensor> active);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "vllm_moet_b200 sm_100a kernels";
+  m.def("rmsnorm_quant", &rmsnorm_quant);
+  m.def("swiglu_quant", &swiglu_quant);
+  m.def("quant_fp8", &quant_fp8);
+  m.def("gemv_fp8", &gemv_fp8);
+  m.def("router_topk", &router_topk);
+  m.def("build_pairs", &build_pairs);
+  m.def("moe_w2_gemv", &moe_w2_gemv);
+  m.def("moe_combine", &moe_combine);
+  m.def("mla_decode", &mla_decode);
+  m.def("mla_combine", &mla_combine);
+  m.def("q_prep", &q_prep);
+  m.def("kv_prep", &kv_prep);
+  m.def("mla_prefill", &mla_prefill);
+  m.def("nvfp4_quant", &nvfp4_quant);
+  m.def("w2_quant_pack", &w2_quant_pack);
+  m.def("argmax_lse", &argmax_lse);
+  m.def("mtp_accept", &mtp_accept);
+  m.def("mtp_finalize", &mtp_finalize);
+}

@@ -1,0 +1,340 @@
+// MLA decode attention in the absorbed (latent) form, over a paged KV cache.
+//
+// Every query row (token t, head h) holds [q_lat (512) | q_rope (64)] where
+// q_lat = W_uk^T q_nope; keys and values are the shared latent rows
+// [c_kv (512) | k_rope (64)] of the cache, so all heads of a token share one
+// KV stream (MQA-like).  One CTA handles all heads of one token for a
+// contiguous share of its context ("split"); a combine kernel merges splits
+// (flash-decoding) and emits the FP8 operand of the W_uv projection.
+//
+// KV cache (bf16): [blocks, 64, 584] bf16 -- 512 latent, 64 rope, 8 pad; the
+// 1168-byte row stride makes ldmatrix conflict-free without a swizzle.  A
+// whole 64-token block (74,752 B) is fetched by one cp.async.bulk
+// (TMA bulk copy, no multicast) completing on an mbarrier; two buffers
+// double-buffer the stream.  S = Q K^T and O += P V use mma.sync bf16
+// m16n8k16 with fp32 accumulation; softmax is online (exp2 domain).
+// All waits are bounded: on timeout the kernel records kTimeout in *status
+// and returns instead of hanging.
+#include "common.cuh"
+#include "torch_glue.h"
+
+namespace moet {
+
+constexpr int kBS = 64;           // tokens per KV block
+constexpr int kRow = 584;         // bf16 elements per cache row
+constexpr int kLat = 512, kQK = 576;
+constexpr int kBlockBytes = kBS * kRow * 2;
+constexpr int kPRow = 72;         // P smem row (bf16), 144 B stride
+
+MOET_DEVICE uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+MOET_DEVICE void mbar_init(uint64_t* bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+MOET_DEVICE void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes));
+}
+MOET_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+MOET_DEVICE void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+MOET_DEVICE void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Bounded wait; returns false on timeout.
+MOET_DEVICE bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  for (uint32_t it = 0; it < (1u << 22); it++)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+struct MlaDecodeArgs {
+  const __nv_bfloat16* q; long long q_tok_stride;     // [T, Hh, 576]
+  const __nv_bfloat16* kv; int n_blocks;               // [blocks, 64, 584]
+  const int* block_table; int bt_stride;               // [seqs, max_blocks]
+  const int* seq_of_tok; const int* pos_of_tok;        // [T]
+  float* o_part; float* ml_part;                       // [S, T, Hh, 512], [S, T, Hh, 2]
+  int T, Hh, nsplit;
+  float scale_log2;                                    // softmax scale * log2(e)
+  int* status;
+};
+
+template <int MT>
+__global__ void __launch_bounds__(256, 1) mla_decode_kernel(MlaDecodeArgs p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __nv_bfloat16* kvs = reinterpret_cast<__nv_bfloat16*>(smem_raw);                 // 2 blocks
+  __nv_bfloat16* qs = kvs + 2 * kBS * kRow;                                         // [16MT][584]
+  __nv_bfloat16* ps = qs + 16 * MT * kRow;                                          // [16MT][72]
+  float* red = reinterpret_cast<float*>(ps + 16 * MT * kPRow);                      // [8][16MT]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red + 8 * 16 * MT);                  // [2]
+
+  const int tok = blockIdx.x, split = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int R = 16 * MT;
+  const int seq = p.seq_of_tok[tok];
+  const int L = p.pos_of_tok[tok] + 1;
+  const int ntiles = (L + kBS - 1) / kBS;
+  const int tps = (ntiles + p.nsplit - 1) / p.nsplit;
+  const int t_begin = split * tps, t_end = min(ntiles, t_begin + tps);
+
+  if (threadIdx.x == 0) { mbar_init(&bars[0], 1); mbar_init(&bars[1], 1); fence_proxy_async(); }
+  // Q rows -> smem (rows >= Hh zero)
+  for (int i = threadIdx.x; i < R * (kQK / 8); i += blockDim.x) {
+    const int r = i / (kQK / 8), c = (i % (kQK / 8)) * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < p.Hh) v = *reinterpret_cast<const uint4*>(p.q + (size_t)tok * p.q_tok_stride + (size_t)r * kQK + c);
+    *reinterpret_cast<uint4*>(qs + r * kRow + c) = v;
+  }
+  __syncthreads();
+
+  auto issue = [&](int tile, int buf) {
+    int blk = p.block_table[(size_t)seq * p.bt_stride + tile];
+    if (blk < 0 || blk >= p.n_blocks) { set_status(p.status, kBadIndex); blk = 0; }
+    mbar_expect_tx(&bars[buf], kBlockBytes);
+    bulk_g2s(kvs + (size_t)buf * kBS * kRow, p.kv + (size_t)blk * kBS * kRow, kBlockBytes, &bars[buf]);
+  };
+  if (threadIdx.x == 0 && t_begin < t_end) issue(t_begin, 0);
+
+  float o[MT][8][4];
+#pragma unroll
+  for (int a = 0; a < MT; a++)
+#pragma unroll
+    for (int b = 0; b < 8; b++) o[a][b][0] = o[a][b][1] = o[a][b][2] = o[a][b][3] = 0.f;
+  float m_run[MT][2], l_run[MT][2];
+#pragma unroll
+  for (int a = 0; a < MT; a++) { m_run[a][0] = m_run[a][1] = -INFINITY; l_run[a][0] = l_run[a][1] = 0.f; }
+
+  uint32_t phase[2] = {0, 0};
+  bool ok = true;
+  for (int tile = t_begin; tile < t_end; tile++) {
+    const int buf = (tile - t_begin) & 1;
+    if (threadIdx.x == 0 && tile + 1 < t_end) { fence_proxy_async(); issue(tile + 1, buf ^ 1); }
+    if (!mbar_wait_bounded(&bars[buf], phase[buf])) { ok = false; }
+    phase[buf] ^= 1;
+    if (!__syncthreads_and(ok)) { set_status(p.status, kTimeout); return; }
+    const __nv_bfloat16* kvt = kvs + (size_t)buf * kBS * kRow;
+
+    // ---- S = Q K^T for positions [8w, 8w+8) of the tile ----
+    float s[MT][4];
+#pragma unroll
+    for (int a = 0; a < MT; a++) s[a][0] = s[a][1] = s[a][2] = s[a][3] = 0.f;
+#pragma unroll 4
+    for (int kk = 0; kk < kQK / 16; kk++) {
+      uint32_t bfrag[2];
+      ldmatrix_x2(bfrag, kvt + (size_t)(warp * 8 + (lane & 7)) * kRow + kk * 16 + ((lane >> 3) & 1) * 8);
+#pragma unroll
+      for (int a = 0; a < MT; a++) {
+        uint32_t afrag[4];
+        ldmatrix_x4(afrag, qs + (size_t)(a * 16 + (lane & 15)) * kRow + kk * 16 + (lane >> 4) * 8);
+        mma_bf16_16816(s[a], afrag, bfrag[0], bfrag[1]);
+      }
+    }
+    // scale + mask, per-warp row max
+    const int pbase = tile * kBS + warp * 8 + 2 * t;
+    float tmax[MT][2];
+#pragma unroll
+    for (int a = 0; a < MT; a++) {
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int pos = pbase + (i & 1);
+        s[a][i] = pos < L ? s[a][i] * p.scale_log2 : -INFINITY;
+      }
+      tmax[a][0] = fmaxf(s[a][0], s[a][1]);
+      tmax[a][1] = fmaxf(s[a][2], s[a][3]);
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        tmax[a][h] = fmaxf(tmax[a][h], __shfl_xor_sync(0xffffffffu, tmax[a][h], 1));
+        tmax[a][h] = fmaxf(tmax[a][h], __shfl_xor_sync(0xffffffffu, tmax[a][h], 2));
+      }
+      if (t == 0) { red[warp * R + a * 16 + g] = tmax[a][0]; red[warp * R + a * 16 + g + 8] = tmax[a][1]; }
+    }
+    __syncthreads();
+    float m_new[MT][2], alpha[MT][2];
+#pragma unroll
+    for (int a = 0; a < MT; a++)
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 8; w++) mx = fmaxf(mx, red[w * R + a * 16 + g + 8 * h]);
+        m_new[a][h] = fmaxf(m_run[a][h], mx);
+        alpha[a][h] = m_new[a][h] == -INFINITY ? 1.f : exp2f(m_run[a][h] - m_new[a][h]);
+      }
+    __syncthreads();  // red reused for row sums
+    // P = exp2(S - m), to smem as bf16; partial row sums
+#pragma unroll
+    for (int a = 0; a < MT; a++) {
+      float e0 = m_new[a][0] == -INFINITY ? 0.f : exp2f(s[a][0] - m_new[a][0]);
+      float e1 = m_new[a][0] == -INFINITY ? 0.f : exp2f(s[a][1] - m_new[a][0]);
+      float e2 = m_new[a][1] == -INFINITY ? 0.f : exp2f(s[a][2] - m_new[a][1]);
+      float e3 = m_new[a][1] == -INFINITY ? 0.f : exp2f(s[a][3] - m_new[a][1]);
+      __nv_bfloat162 p01 = __floats2bfloat162_rn(e0, e1), p23 = __floats2bfloat162_rn(e2, e3);
+      *reinterpret_cast<__nv_bfloat162*>(ps + (a * 16 + g) * kPRow + warp * 8 + 2 * t) = p01;
+      *reinterpret_cast<__nv_bfloat162*>(ps + (a * 16 + g + 8) * kPRow + warp * 8 + 2 * t) = p23;
+      // row sums of the rounded probabilities (what the PV product uses)
+      float r0 = __low2float(p01) + __high2float(p01), r1 = __low2float(p23) + __high2float(p23);
+      r0 += __shfl_xor_sync(0xffffffffu, r0, 1); r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
+      r1 += __shfl_xor_sync(0xffffffffu, r1, 1); r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
+      if (t == 0) { red[warp * R + a * 16 + g] = r0; red[warp * R + a * 16 + g + 8] = r1; }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int a = 0; a < MT; a++)
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) sum += red[w * R + a * 16 + g + 8 * h];
+        l_run[a][h] = l_run[a][h] * alpha[a][h] + sum;
+        m_run[a][h] = m_new[a][h];
+      }
+#pragma unroll
+    for (int a = 0; a < MT; a++)
+#pragma unroll
+      for (int nt = 0; nt < 8; nt++) {
+        o[a][nt][0] *= alpha[a][0]; o[a][nt][1] *= alpha[a][0];
+        o[a][nt][2] *= alpha[a][1]; o[a][nt][3] *= alpha[a][1];
+      }
+    // ---- O += P V for latent dims [64w, 64w+64) ----
+#pragma unroll
+    for (int kk = 0; kk < kBS / 16; kk++) {
+      uint32_t afrag[MT][4];
+#pragma unroll
+      for (int a = 0; a < MT; a++)
+        ldmatrix_x4(afrag[a], ps + (size_t)(a * 16 + (lane & 15)) * kPRow + kk * 16 + (lane >> 4) * 8);
+#pragma unroll
+      for (int np = 0; np < 4; np++) {  // pairs of n8 tiles
+        const int d0 = warp * 64 + np * 16;
+        const int prow = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int dcol = d0 + (lane >> 4) * 8;
+        uint32_t b[4];
+        ldmatrix_x4_trans(b, kvt + (size_t)prow * kRow + dcol);
+#pragma unroll
+        for (int a = 0; a < MT; a++) {
+          mma_bf16_16816(o[a][2 * np], afrag[a], b[0], b[1]);
+          mma_bf16_16816(o[a][2 * np + 1], afrag[a], b[2], b[3]);
+        }
+      }
+    }
+    __syncthreads();  // buffer + P free for the next tile
+  }
+  // ---- write partial state ----
+  const size_t base = ((size_t)split * p.T + tok) * p.Hh;
+#pragma unroll
+  for (int a = 0; a < MT; a++)
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int row = a * 16 + g + 8 * h;
+      if (row >= p.Hh) continue;
+      float* op = p.o_part + (base + row) * kLat + warp * 64;
+#pragma unroll
+      for (int nt = 0; nt < 8; nt++)
+        *reinterpret_cast<float2*>(op + nt * 8 + 2 * t) = make_float2(o[a][nt][2 * h], o[a][nt][2 * h + 1]);
+      if (warp == 0 && t == 0) {
+        p.ml_part[(base + row) * 2] = m_run[a][h];
+        p.ml_part[(base + row) * 2 + 1] = l_run[a][h];
+      }
+    }
+}
+
+// Merge splits; emit bf16 [T, Hh, 512] and/or e4m3 + UE8M0 per-64 scales.
+__global__ void mla_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ ml_part,
+                                   int S, int TH, __nv_bfloat16* __restrict__ out,
+                                   uint8_t* __restrict__ q, uint8_t* __restrict__ qs) {
+  const int row = blockIdx.x;  // (t, h)
+  float M = -INFINITY;
+  for (int s = 0; s < S; s++) M = fmaxf(M, ml_part[((size_t)s * TH + row) * 2]);
+  float denom = 0.f;
+  for (int s = 0; s < S; s++) {
+    const float m = ml_part[((size_t)s * TH + row) * 2];
+    if (m != -INFINITY) denom += exp2f(m - M) * ml_part[((size_t)s * TH + row) * 2 + 1];
+  }
+  const float inv = denom > 0.f ? 1.f / denom : 0.f;
+  // 64 threads x 8 dims
+  const int d0 = threadIdx.x * 8;
+  float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int s = 0; s < S; s++) {
+    const float m = ml_part[((size_t)s * TH + row) * 2];
+    if (m == -INFINITY) continue;
+    const float w = exp2f(m - M) * inv;
+    const float* op = o_part + ((size_t)s * TH + row) * kLat + d0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = fmaf(w, op[i], v[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; i++) v[i] = __bfloat162float(__float2bfloat16(v[i]));
+  if (out) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) out[(size_t)row * kLat + d0 + i] = __float2bfloat16(v[i]);
+  }
+  if (q) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const uint32_t e = ue8m0_for_amax(amax);
+    const float invs = (e >= 1 && e <= 253) ? __uint_as_float((254u - e) << 23) : 0.f;
+    uint8_t b[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) b[i] = f32_to_e4m3(v[i] * invs);
+    *reinterpret_cast<uint2*>(q + (size_t)row * kLat + d0) = *reinterpret_cast<uint2*>(b);
+    if ((threadIdx.x & 7) == 0) qs[(size_t)row * (kLat / 64) + d0 / 64] = (uint8_t)e;
+  }
+}
+
+}  // namespace moet
+
+using namespace moet;
+
+void mla_decode(torch::Tensor q, torch::Tensor kv, torch::Tensor block_table, torch::Tensor seq_of_tok,
+                torch::Tensor pos_of_tok, torch::Tensor o_part, torch::Tensor ml_part, double scale,
+                torch::Tensor status) {
+  const int T = q.size(0), Hh = q.size(1);
+  TORCH_CHECK(q.size(2) == kQK && q.stride(2) == 1 && q.stride(1) == kQK, "mla_decode: q [T, Hh, 576]");
+  TORCH_CHECK(kv.size(1) == kBS && kv.size(2) == kRow && kv.is_contiguous(), "mla_decode: kv [blocks,64,584]");
+  TORCH_CHECK(Hh <= 32, "mla_decode: at most 32 heads per rank");
+  const int S = o_part.size(0);
+  TORCH_CHECK(o_part.size(1) == T && o_part.size(2) == Hh && o_part.size(3) == kLat, "mla_decode: o_part shape");
+  if (T == 0) return;
+  MlaDecodeArgs p;
+  p.q = (const __nv_bfloat16*)q.data_ptr(); p.q_tok_stride = q.stride(0);
+  p.kv = (const __nv_bfloat16*)kv.data_ptr(); p.n_blocks = kv.size(0);
+  p.block_table = block_table.data_ptr<int>(); p.bt_stride = block_table.stride(0);
+  p.seq_of_tok = seq_of_tok.data_ptr<int>(); p.pos_of_tok = pos_of_tok.data_ptr<int>();
+  p.o_part = o_part.data_ptr<float>(); p.ml_part = ml_part.data_ptr<float>();
+  p.T = T; p.Hh = Hh; p.nsplit = S;
+  p.scale_log2 = (float)(scale * 1.4426950408889634);
+  p.status = status.data_ptr<int>();
+  auto stream = at::cuda::getCurrentCUDAStream();
+  dim3 grid(T, S);
+  if (Hh <= 16) {
+    const int MT = 1;
+    size_t smem = (size_t)(2 * kBS * kRow + 16 * MT * kRow + 16 * MT * kPRow) * 2 + 8 * 16 * MT * 4 + 16;
+    cudaFuncSetAttribute(mla_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    mla_decode_kernel<1><<<grid, 256, smem, stream>>>(p);
+  } else {
+    const int MT = 2;
+    size_t smem = (size_t)(2 * kBS * kRow + 16 * MT * kRow + 16 * MT * kPRow) * 2 + 8 * 16 * MT * 4 + 16;
+    cudaFuncSetAttribute(mla_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    mla_decode_kernel<2><<<grid, 256, smem, stream>>>(p);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void mla_combine(torch::Tensor o_part, torch::Tensor ml_part, c10::optional<torch::Tensor> out,
+                 c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> qs) {
+  const int S = o_part.size(0), TH = o_part.size(1) * o_part.size(2);
+  if (TH == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  mla_combine_kernel<<<TH, 64, 0, stream>>>(o_part.data_ptr<float>(), ml_part.data_ptr<float>(), S, TH,
+                                            (__nv_bfloat16*)opt_ptr(out), (uint8_t*)opt_ptr(q),
+                                            (uint8_t*)opt_ptr(qs));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

@@ -1,0 +1,218 @@
+// Router top-k and the expert pair-list builder.
+//
+// Router (one warp per token): sigmoid scores with a selection bias
+// ("noaux" correction, DeepSeek-V3/V4 style) and optional group-limited
+// selection, or softmax scores; top-k by repeated warp argmax with ties
+// broken toward the lower expert id; weights renormalised and scaled.
+//
+// Pair-list builder (one CTA): groups the T*k routings by expert and cuts
+// each expert's rows into "pairs" of at most MB rows -- the work items of
+// the expert GEMV/GEMM (reference: moe_align_block_size + the Triton desc
+// builders, P:6198-6254, P:7389).  Everything stays on the device so a
+// captured CUDA graph replays any routing.  Numerics do not depend on the
+// order of rows inside an expert (each output column is independent).
+#include "common.cuh"
+#include "torch_glue.h"
+
+namespace moet {
+
+constexpr int kMaxE = 512;
+
+__global__ void router_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+                                   int T, int E, int k, int sigmoid, int n_group, int topk_group,
+                                   int norm, float scaling, int* __restrict__ ids, float* __restrict__ wts) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  constexpr int PER = kMaxE / 32;
+  float score[PER], sel[PER];
+  const int per = (E + 31) / 32;
+  const float* lg = logits + (size_t)warp * E;
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < PER; i++) {
+    const int e = lane + 32 * i;
+    float v = (i < per && e < E) ? lg[e] : -INFINITY;
+    score[i] = v;
+    mx = fmaxf(mx, v);
+  }
+  if (sigmoid) {
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+      const int e = lane + 32 * i;
+      if (i < per && e < E) {
+        score[i] = 1.f / (1.f + __expf(-score[i]));
+        sel[i] = score[i] + (bias ? bias[e] : 0.f);
+      } else { score[i] = 0.f; sel[i] = -INFINITY; }
+    }
+  } else {
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+      const int e = lane + 32 * i;
+      float v = (i < per && e < E) ? __expf(score[i] - mx) : 0.f;
+      score[i] = v; sum += v;
+    }
+    sum = warp_sum(sum);
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+      const int e = lane + 32 * i;
+      score[i] /= sum;
+      sel[i] = (i < per && e < E) ? score[i] : -INFINITY;
+    }
+  }
+  if (n_group > 1 && topk_group < n_group) {
+    // group score = sum of the two best selection scores in the group; keep topk_group groups
+    const int gsize = E / n_group;
+    __shared__ float gscore_s[8][64];
+    float* gscore = gscore_s[threadIdx.x >> 5];
+    __syncwarp();
+    // Compute group scores cooperatively: each lane owns experts lane+32i.
+    for (int gi = 0; gi < n_group; gi++) {
+      float b1 = -INFINITY, b2 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < PER; i++) {
+        const int e = lane + 32 * i;
+        if (i < per && e < E && e / gsize == gi) {
+          float v = sel[i];
+          if (v > b1) { b2 = b1; b1 = v; } else if (v > b2) b2 = v;
+        }
+      }
+      // warp-merge top-2
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        float o1 = __shfl_xor_sync(0xffffffffu, b1, o), o2 = __shfl_xor_sync(0xffffffffu, b2, o);
+        float n1 = fmaxf(b1, o1);
+        float n2 = fmaxf(fminf(b1, o1), fmaxf(b2, o2));
+        b1 = n1; b2 = n2;
+      }
+      if (lane == 0) gscore[gi] = b1 + (gsize > 1 ? b2 : 0.f);
+    }
+    __syncwarp();
+    // choose topk_group groups (ties -> lower group id)
+    unsigned long long keep = 0;
+    for (int r = 0; r < topk_group; r++) {
+      int best = -1; float bv = -INFINITY;
+      for (int gi = 0; gi < n_group; gi++)
+        if (!((keep >> gi) & 1ull) && (best < 0 || gscore[gi] > bv)) { best = gi; bv = gscore[gi]; }
+      keep |= 1ull << best;
+    }
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+      const int e = lane + 32 * i;
+      if (i < per && e < E && !((keep >> (e / gsize)) & 1ull)) sel[i] = -INFINITY;
+    }
+  }
+  float wsum = 0.f;
+  float myw = 0.f; int myid = 0;
+  for (int r = 0; r < k; r++) {
+    float bv = -INFINITY; int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+      const int e = lane + 32 * i;
+      if (i < per && e < E && (sel[i] > bv || (sel[i] == bv && e < bi))) { bv = sel[i]; bi = e; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    // owner lane reads the raw score and removes the expert from selection
+    float w = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+      const int e = lane + 32 * i;
+      if (e == bi) { w = score[i]; sel[i] = -INFINITY; }
+    }
+    w = __shfl_sync(0xffffffffu, w, bi & 31);
+    wsum += w;
+    if (lane == r) { myw = w; myid = bi; }
+  }
+  if (lane < k) {
+    float w = myw;
+    if (norm) w = w / (wsum + 1e-20f);
+    ids[(size_t)warp * k + lane] = myid;
+    wts[(size_t)warp * k + lane] = w * scaling;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Pair-list builder.  outputs:
+//   sorted_tok[R]   token of each expert-sorted row
+//   pos_of[R]       routing r (= t*k + j) -> sorted row
+//   pairs[P] int4   {expert, first sorted row, n rows (<= MB), 0}
+//   n_pairs[1]
+__global__ void build_pairs_kernel(const int* __restrict__ topk_ids, int R, int k, int E, int MB,
+                                   int* __restrict__ rank_scratch, int* __restrict__ sorted_tok,
+                                   int* __restrict__ pos_of, int4* __restrict__ pairs,
+                                   int* __restrict__ n_pairs, int* __restrict__ status) {
+  __shared__ int cnt[kMaxE];
+  __shared__ int start[kMaxE];
+  __shared__ int pstart[kMaxE];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    int e = topk_ids[r];
+    if (e < 0 || e >= E) { set_status(status, kBadIndex); e = 0; }
+    rank_scratch[r] = atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int s = 0, ps = 0;
+    for (int e = 0; e < E; e++) {
+      start[e] = s; pstart[e] = ps;
+      s += cnt[e];
+      ps += (cnt[e] + MB - 1) / MB;
+    }
+    *n_pairs = ps;
+  }
+  __syncthreads();
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    int e = topk_ids[r];
+    if (e < 0 || e >= E) e = 0;
+    const int pos = start[e] + rank_scratch[r];
+    sorted_tok[pos] = r / k;
+    pos_of[r] = pos;
+  }
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int c = cnt[e];
+    for (int i = 0; i * MB < c; i++)
+      pairs[pstart[e] + i] = make_int4(e, start[e] + i * MB, min(MB, c - i * MB), 0);
+  }
+}
+
+}  // namespace moet
+
+using namespace moet;
+
+void router_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_t k, bool sigmoid,
+                 int64_t n_group, int64_t topk_group, bool norm, double scaling, torch::Tensor ids,
+                 torch::Tensor wts) {
+  const int T = logits.size(0), E = logits.size(1);
+  TORCH_CHECK(E <= kMaxE && k <= 32, "router_topk: E <= 512, k <= 32");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.is_contiguous(), "logits f32 contiguous");
+  TORCH_CHECK(n_group <= 64, "router_topk: n_group <= 64");
+  if (T == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int warps = 8;
+  router_topk_kernel<<<(T + warps - 1) / warps, warps * 32, 0, stream>>>(
+      logits.data_ptr<float>(), bias.has_value() && bias->defined() ? bias->data_ptr<float>() : nullptr,
+      T, E, (int)k, sigmoid ? 1 : 0, (int)n_group, (int)topk_group, norm ? 1 : 0, (float)scaling,
+      ids.data_ptr<int>(), wts.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void build_pairs(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor rank_scratch,
+                 torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
+                 torch::Tensor status) {
+  const int T = topk_ids.size(0), k = topk_ids.size(1), R = T * k;
+  TORCH_CHECK(E <= kMaxE, "build_pairs: E <= 512");
+  TORCH_CHECK(pairs.size(0) >= R / MB + std::min<int64_t>(E, R), "build_pairs: pairs buffer too small");
+  auto stream = at::cuda::getCurrentCUDAStream();
+  build_pairs_kernel<<<1, 1024, 0, stream>>>(topk_ids.data_ptr<int>(), R, k, (int)E, (int)MB,
+                                             rank_scratch.data_ptr<int>(), sorted_tok.data_ptr<int>(),
+                                             pos_of.data_ptr<int>(), (int4*)pairs.data_ptr<int>(),
+                                             n_pairs.data_ptr<int>(), status.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

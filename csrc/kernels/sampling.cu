@@ -1,0 +1,125 @@
+// Sampling-side kernels of the decode step.
+//   argmax_lse : per row argmax (ties -> lowest id) and log-sum-exp of the logits;
+//                max_prob = exp(max - lse) is the confidence-gate signal
+//                (reference gate P:11554-11628).
+//   mtp_accept : greedy verification of k MTP drafts: accepted = longest prefix with
+//                draft[j] == target[j]; emits target[0..accepted]; reports per-row
+//                acceptance.  All state stays on the device (graph-replayable).
+//   mtp_finalize: advances the per-sequence position and builds the next step's
+//                 input tokens [target[a], draft_1 .. draft_k].
+#include "common.cuh"
+#include "torch_glue.h"
+
+namespace moet {
+
+template <typename T>
+__global__ void argmax_lse_kernel(const T* __restrict__ logits, long long stride, int V,
+                                  int* __restrict__ ids, float* __restrict__ lse, float* __restrict__ maxv) {
+  const int row = blockIdx.x;
+  const T* x = logits + (size_t)row * stride;
+  float bv = -INFINITY; int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = (float)x[i];
+    if (v > bv) { bv = v; bi = i; }
+  }
+  __shared__ float sv[32]; __shared__ int si[32]; __shared__ float ssum[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o); const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (l == 0) { sv[w] = bv; si[w] = bi; }
+  __syncthreads();
+  if (w == 0) {
+    bv = l < nw ? sv[l] : -INFINITY; bi = l < nw ? si[l] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o); const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (l == 0) { sv[0] = bv; si[0] = bi; }
+  }
+  __syncthreads();
+  const float m = sv[0];
+  if (lse) {
+    float s = 0.f;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) s += __expf((float)x[i] - m);
+    s = warp_sum(s);
+    if (l == 0) ssum[w] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float tot = 0.f;
+      for (int i = 0; i < nw; i++) tot += ssum[i];
+      lse[row] = m + __logf(tot);
+    }
+  }
+  if (threadIdx.x == 0) { ids[row] = si[0]; if (maxv) maxv[row] = m; }
+}
+
+// targets [B, 1+k] (argmax of the verify rows), tokens [B, 1+k] (this step's inputs;
+// cols 1..k are the drafts).  out_tokens [B, 1+k], n_acc [B].
+__global__ void mtp_accept_kernel(const int* __restrict__ targets, const int* __restrict__ tokens, int B, int kp1,
+                                  int* __restrict__ out_tokens, int* __restrict__ n_acc,
+                                  const int* __restrict__ active) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  int a = 0;
+  if (!active || active[b]) {
+    while (a + 1 < kp1 && tokens[b * kp1 + a + 1] == targets[b * kp1 + a]) a++;
+  }
+  for (int j = 0; j < kp1; j++) out_tokens[b * kp1 + j] = j <= a ? targets[b * kp1 + j] : -1;
+  n_acc[b] = a;
+}
+
+// next inputs: tokens[b] = [targets[b, a], drafts[b, 0..k-1]]; seq_pos[b] += a + 1.
+__global__ void mtp_finalize_kernel(const int* __restrict__ targets, const int* __restrict__ n_acc,
+                                    const int* __restrict__ drafts, int B, int kp1, int* __restrict__ tokens,
+                                    int* __restrict__ seq_pos, const int* __restrict__ active) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  if (active && !active[b]) return;
+  const int a = n_acc[b];
+  tokens[b * kp1] = targets[b * kp1 + a];
+  for (int j = 1; j < kp1; j++) tokens[b * kp1 + j] = drafts[b * (kp1 - 1) + (j - 1)];
+  seq_pos[b] += a + 1;
+}
+
+}  // namespace moet
+
+using namespace moet;
+
+void argmax_lse(torch::Tensor logits, torch::Tensor ids, c10::optional<torch::Tensor> lse,
+                c10::optional<torch::Tensor> maxv) {
+  const int R = logits.size(0), V = logits.size(1);
+  TORCH_CHECK(logits.stride(1) == 1, "argmax_lse: inner stride 1");
+  if (R == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (logits.scalar_type() == at::kFloat)
+    argmax_lse_kernel<float><<<R, 1024, 0, stream>>>(logits.data_ptr<float>(), logits.stride(0), V, ids.data_ptr<int>(),
+                                                     (float*)opt_ptr(lse), (float*)opt_ptr(maxv));
+  else
+    argmax_lse_kernel<__nv_bfloat16><<<R, 1024, 0, stream>>>((const __nv_bfloat16*)logits.data_ptr(), logits.stride(0), V,
+                                                             ids.data_ptr<int>(), (float*)opt_ptr(lse), (float*)opt_ptr(maxv));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void mtp_accept(torch::Tensor targets, torch::Tensor tokens, torch::Tensor out_tokens, torch::Tensor n_acc,
+                c10::optional<torch::Tensor> active) {
+  const int B = targets.size(0), kp1 = targets.size(1);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  mtp_accept_kernel<<<(B + 127) / 128, 128, 0, stream>>>(targets.data_ptr<int>(), tokens.data_ptr<int>(), B, kp1,
+                                                         out_tokens.data_ptr<int>(), n_acc.data_ptr<int>(),
+                                                         (const int*)opt_ptr(active));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void mtp_finalize(torch::Tensor targets, torch::Tensor n_acc, torch::Tensor drafts, torch::Tensor tokens,
+                  torch::Tensor seq_pos, c10::optional<torch::Tensor> active) {
+  const int B = targets.size(0), kp1 = targets.size(1);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  mtp_finalize_kernel<<<(B + 127) / 128, 128, 0, stream>>>(targets.data_ptr<int>(), n_acc.data_ptr<int>(),
+                                                           drafts.data_ptr<int>(), B, kp1, tokens.data_ptr<int>(),
+                                                           seq_pos.data_ptr<int>(), (const int*)opt_ptr(active));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

@@ -1,0 +1,439 @@
+"""Native (sm_100a) model executor: prefill, MTP speculative decode steps and
+CUDA-graph capture of the decode step.
+
+All per-step state lives on the device (input tokens, positions, block
+tables, acceptance), so one captured graph per batch bucket replays a whole
+decode step -- main model over B*(1+k) verify rows, greedy acceptance, two
+chained MTP draft passes and the advance of every sequence -- with no host
+round trip inside.  The host only reads the emitted tokens back.
+
+Kernel order of one decoder layer (T rows):
+  rmsnorm_quant -> gemv(qkv_a) -> rmsnorm_quant(q_a) | kv_prep(norm, rope, cache write)
+  -> gemv(q_b) -> q_prep(rope, fp8 q_nope) -> gemv_batched(W_uk^T) -> mla_decode -> mla_combine(fp8)
+  -> gemv_batched(W_uv) -> quant -> gemv(o, +residual)
+  -> rmsnorm_quant(bf16 + fp8 natural + fp8 w2 layout) -> router logits -> router_topk -> build_pairs
+  -> moe_w2_gemv(w13) -> swiglu_quant -> moe_w2_gemv(w2) ; shared expert gemvs -> moe_combine(+residual)
+Prefill replaces the absorbed attention with the non-absorbed flash kernel.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from ..config import EngineConfig, ModelConfig
+from ..models.reference import rope_cos_sin
+from ..models.weights import LayerWeights, ModelWeights
+from ..ops import native
+
+KV_BLOCK = 64
+BF16_ROW = 584      # bf16 elements per cache row (512 latent + 64 rope + 8 pad)
+NVFP4_ROW = 352     # bytes per NVFP4 row
+
+
+class Workspace:
+    """Grow-only named device buffers; frozen once a graph has been captured."""
+
+    def __init__(self, device):
+        self.device = device
+        self.bufs = {}
+        self.frozen = False
+
+    def get(self, name, shape, dtype):
+        n = 1
+        for s in shape:
+            n *= s
+        b = self.bufs.get((name, dtype))
+        if b is None or b.numel() < n:
+            if self.frozen:
+                raise RuntimeError(f"workspace {name} must grow to {shape} after graph capture")
+            b = torch.empty(max(n, 1), dtype=dtype, device=self.device)
+            self.bufs[(name, dtype)] = b
+        return b[:n].view(*shape)
+
+
+@dataclass
+class StepCtx:
+    T: int
+    pos: torch.Tensor            # [T] int32
+    seq: torch.Tensor            # [T] int32 (row into block_table)
+    slot: torch.Tensor           # [T] int64
+    block_table: torch.Tensor    # [S, max_blocks] int32
+    mode: str                    # "decode" | "prefill"
+    cu_seqlens: Optional[torch.Tensor] = None
+    max_len: int = 0
+    mb: int = 8                  # rows per expert pair
+
+
+class NativeRunner:
+    def __init__(self, mw: ModelWeights, ecfg: EngineConfig, num_blocks: int, device="cuda"):
+        self.C = native()
+        self.mw = mw
+        self.cfg: ModelConfig = mw.cfg
+        self.ecfg = ecfg
+        self.dev = torch.device(device)
+        self.k = ecfg.num_speculative_tokens if mw.mtp is not None else 0
+        self.Hh = self.cfg.num_heads // mw.tp_size
+        cfg = self.cfg
+        self.num_blocks = num_blocks
+        self.kv_mode = 2 if ecfg.kv_cache_dtype == "nvfp4" else 1
+        if self.kv_mode == 2:
+            raise NotImplementedError("NVFP4 KV decode attention is not wired in the native runner yet")
+        n_cache = len(mw.layers) + (1 if mw.mtp is not None else 0)
+        self.kv = [torch.zeros(num_blocks, KV_BLOCK, BF16_ROW, dtype=torch.bfloat16, device=self.dev)
+                   for _ in range(n_cache)]
+        self.cos_sin = rope_cos_sin(cfg, ecfg.max_model_len + 64, self.dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        self.miss = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        self.ws_decode = Workspace(self.dev)
+        self.ws_prefill = Workspace(self.dev)
+        self.ws = self.ws_decode
+        self.scale = 1.0 / math.sqrt(cfg.qk_head_dim)
+        self.graphs = {}
+        self.tp_group = None
+        self.nsplit = 8
+
+    # ------------------------------------------------------------------ helpers
+    def _fp8(self, name, T, K):
+        return (self.ws.get(name + ".q", (T, K), torch.uint8), self.ws.get(name + ".s", (T, K // 64), torch.uint8))
+
+    def _gemv(self, aq, as_, lin, out, resid=None):
+        self.C.gemv_fp8(aq, as_, lin.w, lin.s, out, resid)
+
+    def _tp_allreduce(self, t):
+        if self.tp_group is not None:
+            torch.distributed.all_reduce(t, group=self.tp_group)
+
+    # ------------------------------------------------------------------ layer
+    def _attention(self, lw: LayerWeights, x, ctx: StepCtx, cache, li, out):
+        cfg, C, T, Hh = self.cfg, self.C, ctx.T, self.Hh
+        H, ql, lat, rope, nope, vd = cfg.hidden, cfg.q_lora_rank, cfg.kv_lora_rank, cfg.qk_rope_dim, cfg.qk_nope_dim, cfg.v_head_dim
+        hq, hs = self._fp8("h", T, H)
+        C.rmsnorm_quant(x, None, None, lw.attn_norm, cfg.rms_eps, None, hq, hs, None, None, 0)
+        qkva = self.ws.get("qkva", (T, ql + lat + rope), torch.bfloat16)
+        self._gemv(hq, hs, lw.qkv_a, qkva)
+        qaq, qas = self._fp8("qa", T, ql)
+        C.rmsnorm_quant(qkva[:, :ql], None, None, lw.q_a_norm, cfg.rms_eps, None, qaq, qas, None, None, 0)
+        qb = self.ws.get("qb", (T, Hh * (nope + rope)), torch.bfloat16)
+        self._gemv(qaq, qas, lw.q_b, qb)
+        ovq, ovs = self._fp8("ov", T, Hh * vd)
+        if ctx.mode == "decode":
+            C.kv_prep(qkva[:, ql:], lat, rope, lw.kv_a_norm, cfg.rms_eps, ctx.pos, self.cos_sin, ctx.slot,
+                      self.kv_mode, cache, None, None, None, None, self.status)
+            qnq = self.ws.get("qn.q", (T, Hh, nope), torch.uint8)
+            qns = self.ws.get("qn.s", (T, Hh, nope // 64), torch.uint8)
+            qcat = self.ws.get("qcat", (T, Hh, lat + rope), torch.bfloat16)
+            C.q_prep(qb, Hh, nope, rope, ctx.pos, self.cos_sin, qnq, qns, qcat, lat, None)
+            C.gemv_fp8(qnq.permute(1, 0, 2), qns.permute(1, 0, 2), lw.w_uk_t.w, lw.w_uk_t.s,
+                       qcat[:, :, :lat].permute(1, 0, 2), None)
+            S = self.nsplit
+            opart = self.ws.get("opart", (S, T, Hh, lat), torch.float32)
+            mlp = self.ws.get("mlpart", (S, T, Hh, 2), torch.float32)
+            C.mla_decode(qcat, cache, ctx.block_table, ctx.seq, ctx.pos, opart, mlp, self.scale, self.status)
+            olq = self.ws.get("ol.q", (T, Hh, lat), torch.uint8)
+            ols = self.ws.get("ol.s", (T, Hh, lat // 64), torch.uint8)
+            C.mla_combine(opart, mlp, None, olq, ols)
+            ov = self.ws.get("ov", (T, Hh * vd), torch.bfloat16)
+            C.gemv_fp8(olq.permute(1, 0, 2), ols.permute(1, 0, 2), lw.w_uv.w, lw.w_uv.s,
+                       ov.view(T, Hh, vd).permute(1, 0, 2), None)
+            C.quant_fp8(ov, 0, ovq, ovs)
+        else:
+            latq, lats = self._fp8("lat", T, lat)
+            kr = self.ws.get("kr", (T, rope), torch.bfloat16)
+            C.kv_prep(qkva[:, ql:], lat, rope, lw.kv_a_norm, cfg.rms_eps, ctx.pos, self.cos_sin, ctx.slot,
+                      self.kv_mode, cache, None, kr, latq, lats, self.status)
+            kvb = self.ws.get("kvb", (T, Hh * (nope + vd)), torch.bfloat16)
+            self._gemv(latq, lats, lw.kv_b, kvb)
+            qf = self.ws.get("qfull", (T, Hh, nope + rope), torch.bfloat16)
+            C.q_prep(qb, Hh, nope, rope, ctx.pos, self.cos_sin, None, None, None, 0, qf)
+            C.mla_prefill(qf, kvb.view(T, Hh, nope + vd), kr, ctx.cu_seqlens, ctx.max_len, self.scale,
+                          ovq, ovs, None)
+        if self.tp_group is None:
+            self._gemv(ovq, ovs, lw.o, out, x)
+        else:
+            part = self.ws.get("attn_part", (T, H), torch.bfloat16)
+            self._gemv(ovq, ovs, lw.o, part)
+            self._tp_allreduce(part)
+            torch.add(x, part, out=out)
+
+    def _ffn(self, lw: LayerWeights, x, ctx: StepCtx, out):
+        cfg, C, T = self.cfg, self.C, ctx.T
+        H = cfg.hidden
+        hb = self.ws.get("hb", (T, H), torch.bfloat16)
+        hq, hs = self._fp8("h", T, H)
+        if not lw.is_moe:
+            C.rmsnorm_quant(x, None, None, lw.ffn_norm, cfg.rms_eps, None, hq, hs, None, None, 0)
+            I2 = lw.gate_up.w.shape[0]
+            gu = self.ws.get("gu", (T, I2), torch.float32)
+            self._gemv(hq, hs, lw.gate_up, gu)
+            aq, as_ = self._fp8("act", T, I2 // 2)
+            C.swiglu_quant(gu, 0.0, None, 0, aq, as_)
+            self._ffn_out(lw.down, aq, as_, x, out, T)
+            return
+        h2q, h2s = self._fp8("h2", T, H)
+        C.rmsnorm_quant(x, None, None, lw.ffn_norm, cfg.rms_eps, hb, hq, hs, h2q, h2s, 0)
+        E, k = cfg.num_experts, cfg.top_k
+        logits = self.ws.get("rlogits", (T, E), torch.float32)
+        torch.mm(hb.float(), lw.router_w.t(), out=logits)
+        ids = self.ws.get("topk_ids", (T, k), torch.int32)
+        wts = self.ws.get("topk_w", (T, k), torch.float32)
+        C.router_topk(logits, lw.router_bias, k, cfg.router == "sigmoid", cfg.n_group, cfg.topk_group,
+                      cfg.norm_topk_prob, cfg.routed_scaling, ids, wts)
+        R = T * k
+        MB = ctx.mb
+        P = R // MB + min(E, R)
+        rank = self.ws.get("rank", (R,), torch.int32)
+        stok = self.ws.get("stok", (R,), torch.int32)
+        posof = self.ws.get("posof", (R,), torch.int32)
+        pairs = self.ws.get("pairs", (P, 4), torch.int32)
+        npairs = self.ws.get("npairs", (1,), torch.int32)
+        C.build_pairs(ids, E, MB, rank, stok, posof, pairs, npairs, self.status)
+        ex = lw.experts
+        L = ex.layout
+        I = L.I
+        c13 = self.ws.get("c13", (R, 2 * I), torch.float32)
+        C.moe_w2_gemv(h2q, h2s, stok, pairs, npairs, ex.pool, L.off_codes13, L.off_sc13, ex.slot_table, c13,
+                      2 * I, H, MB, self.miss)
+        a2q, a2s = self._fp8("a2", R, I)
+        C.swiglu_quant(c13, cfg.swiglu_limit or 0.0, None, 1, a2q, a2s)
+        y2 = self.ws.get("y2", (R, H), torch.float32)
+        C.moe_w2_gemv(a2q, a2s, None, pairs, npairs, ex.pool, L.off_codes2, L.off_sc2, ex.slot_table, y2,
+                      H, I, MB, self.miss)
+        sh = None
+        if lw.shared_gate_up is not None:
+            Is2 = lw.shared_gate_up.w.shape[0]
+            sgu = self.ws.get("sgu", (T, Is2), torch.float32)
+            self._gemv(hq, hs, lw.shared_gate_up, sgu)
+            sq, ss = self._fp8("sact", T, Is2 // 2)
+            C.swiglu_quant(sgu, cfg.swiglu_limit or 0.0, None, 0, sq, ss)
+            sh = self.ws.get("sh", (T, H), torch.bfloat16)
+            self._gemv(sq, ss, lw.shared_down, sh)
+        if self.tp_group is None:
+            C.moe_combine(y2, posof, wts, x, sh, out, None)
+        else:
+            part = self.ws.get("moe_part", (T, H), torch.bfloat16)
+            C.moe_combine(y2, posof, wts, None, sh, part, None)
+            self._tp_allreduce(part)
+            torch.add(x, part, out=out)
+
+    def _ffn_out(self, lin, aq, as_, x, out, T):
+        if self.tp_group is None:
+            self._gemv(aq, as_, lin, out, x)
+        else:
+            part = self.ws.get("ffn_part", (T, self.cfg.hidden), torch.bfloat16)
+            self._gemv(aq, as_, lin, part)
+            self._tp_allreduce(part)
+            torch.add(x, part, out=out)
+
+    def _layer(self, lw, x, ctx, cache, li):
+        H = self.cfg.hidden
+        x2 = self.ws.get("x_mid", (ctx.T, H), torch.bfloat16)
+        self._attention(lw, x, ctx, cache, li, x2)
+        x3 = self.ws.get("x_a" if li % 2 == 0 else "x_b", (ctx.T, H), torch.bfloat16)
+        self._ffn(lw, x2, ctx, x3)
+        return x3
+
+    # ------------------------------------------------------------------ model pieces
+    def _main(self, tokens, ctx: StepCtx):
+        x = torch.nn.functional.embedding(tokens.long(), self.mw.embed)
+        xin = self.ws.get("x_in", (ctx.T, self.cfg.hidden), torch.bfloat16)
+        xin.copy_(x)
+        x = xin
+        for li, lw in enumerate(self.mw.layers):
+            x = self._layer(lw, x, ctx, self.kv[li], li)
+        return x
+
+    def _final(self, x, rows, tag):
+        """final RMSNorm -> (normed hidden bf16 [T,H], logits f32 [T,V])."""
+        cfg, C = self.cfg, self.C
+        T = x.shape[0]
+        hid = self.ws.get(tag + ".hid", (T, cfg.hidden), torch.bfloat16)
+        fq, fs = self._fp8(tag + ".f", T, cfg.hidden)
+        C.rmsnorm_quant(x, None, None, self.mw.final_norm if tag == "main" else self.mw.mtp.head_norm,
+                        cfg.rms_eps, hid, fq, fs, None, None, 0)
+        logits = self.ws.get(tag + ".logits", (T, cfg.vocab), torch.float32)
+        self._gemv(fq, fs, self.mw.lm_head, logits)
+        return hid, logits
+
+    def _mtp(self, hidden, next_tokens, ctx: StepCtx):
+        """MTP module over rows (h_i, token_{i+1}) -> (head-normed hidden, logits)."""
+        cfg, C, m = self.cfg, self.C, self.mw.mtp
+        T, H = ctx.T, cfg.hidden
+        emb = torch.nn.functional.embedding(next_tokens.long(), self.mw.embed)
+        ehq = self.ws.get("eh.q", (T, 2 * H), torch.uint8)
+        ehs = self.ws.get("eh.s", (T, 2 * H // 64), torch.uint8)
+        C.rmsnorm_quant(emb, None, None, m.enorm, cfg.rms_eps, None, ehq, ehs, None, None, 2 * H)
+        C.rmsnorm_quant(hidden, None, None, m.hnorm, cfg.rms_eps, None, ehq[:, H:], ehs[:, H // 64:], None, None,
+                        2 * H)
+        xm = self.ws.get("xm", (T, H), torch.bfloat16)
+        self._gemv(ehq, ehs, m.eh_proj, xm)
+        x = self._layer(m.layer, xm, ctx, self.kv[-1], 0)
+        return self._final(x, None, "mtp")
+
+    # ------------------------------------------------------------------ prefill
+    @torch.no_grad()
+    def prefill(self, prompts: list, block_tables: list, seq_rows: list, state):
+        """Prefill whole prompts (one chunk each); fills main + MTP caches and the
+        decode state rows `seq_rows` (tokens, positions, drafts).  Returns the
+        first generated token of each prompt."""
+        self.ws = self.ws_prefill
+        try:
+            return self._prefill(prompts, block_tables, seq_rows, state)
+        finally:
+            self.ws = self.ws_decode
+
+    def _prefill(self, prompts, block_tables, seq_rows, state):
+        dev, C = self.dev, self.C
+        lens = [len(p) for p in prompts]
+        T = sum(lens)
+        toks = torch.tensor([t for p in prompts for t in p], dtype=torch.int32, device=dev)
+        pos = torch.cat([torch.arange(n, dtype=torch.int32) for n in lens]).to(dev)
+        seq = torch.cat([torch.full((n,), i, dtype=torch.int32) for i, n in enumerate(lens)]).to(dev)
+        bt = torch.tensor(block_tables, dtype=torch.int32, device=dev)
+        slot = (bt[seq.long(), (pos // KV_BLOCK).long()].long() * KV_BLOCK + (pos % KV_BLOCK).long())
+        cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=dev)
+        ctx = StepCtx(T=T, pos=pos, seq=seq, slot=slot, block_table=bt, mode="prefill", cu_seqlens=cu,
+                      max_len=max(lens), mb=32)
+        x = self._main(toks, ctx)
+        last = (cu[1:] - 1).long()
+        xl = x[last].contiguous()
+        hid_last, logits = self._final(xl, None, "main")
+        tgt = self.ws.get("pf.tgt", (len(prompts),), torch.int32)
+        C.argmax_lse(logits, tgt, None, None)
+        B = len(prompts)
+        if self.k == 0:
+            state.set_rows(seq_rows, tgt, torch.tensor(lens, dtype=torch.int32, device=dev), None)
+            return tgt
+        # full hidden for the MTP pass: final norm over all rows
+        hid_all = self.ws.get("pf.hid", (T, self.cfg.hidden), torch.bfloat16)
+        C.rmsnorm_quant(x, None, None, self.mw.final_norm, self.cfg.rms_eps, hid_all, None, None, None, None, 0)
+        nxt = torch.empty_like(toks)
+        nxt[:-1] = toks[1:]
+        nxt[last] = tgt
+        mh, mlog = self._mtp(hid_all, nxt, ctx)
+        drafts = torch.empty(B, self.k, dtype=torch.int32, device=dev)
+        d = self.ws.get("pf.d", (T,), torch.int32)
+        # only the last row of each prompt matters; argmax over those rows
+        ml = mlog[last].contiguous()
+        d1 = self.ws.get("pf.d1", (B,), torch.int32)
+        C.argmax_lse(ml, d1, None, None)
+        drafts[:, 0] = d1
+        h_prev = mh[last].contiguous()
+        cur_pos = torch.tensor(lens, dtype=torch.int32, device=dev)  # position of the first generated token
+        prev_tok = d1
+        for j in range(1, self.k):
+            p2 = cur_pos + (j - 1)
+            s2 = torch.arange(B, dtype=torch.int32, device=dev)
+            slot2 = bt[s2.long(), (p2 // KV_BLOCK).long()].long() * KV_BLOCK + (p2 % KV_BLOCK).long()
+            ctx2 = StepCtx(T=B, pos=p2, seq=s2, slot=slot2, block_table=bt, mode="decode", mb=8)
+            h_prev, lg = self._mtp(h_prev.clone(), prev_tok, ctx2)
+            dj = self.ws.get("pf.dj", (B,), torch.int32)
+            C.argmax_lse(lg, dj, None, None)
+            drafts[:, j] = dj
+            prev_tok = dj.clone()
+        state.set_rows(seq_rows, tgt, cur_pos, drafts)
+        return tgt
+
+    # ------------------------------------------------------------------ decode
+    def decode_body(self, st):
+        """One MTP decode step over the device state `st` (all tensors static)."""
+        C, k = self.C, self.k
+        B = st.B
+        kp1 = k + 1
+        T = B * kp1
+        pos = (st.seq_pos[:, None] + st.arange_kp1[None, :]).reshape(-1)
+        blk = st.block_table.gather(1, (pos // KV_BLOCK).long().view(B, kp1)).reshape(-1)
+        slot = blk.long() * KV_BLOCK + (pos % KV_BLOCK).long()
+        slot = torch.where(st.active_rows, slot, torch.full_like(slot, -1))
+        ctx = StepCtx(T=T, pos=pos.int(), seq=st.seq_rows, slot=slot, block_table=st.block_table, mode="decode",
+                      mb=8 if T * self.cfg.top_k <= 256 else 16)
+        x = self._main(st.tokens.view(-1), ctx)
+        hid, logits = self._final(x, None, "main")
+        C.argmax_lse(logits, st.targets.view(-1), None, None)
+        C.mtp_accept(st.targets, st.tokens, st.out_tokens, st.n_acc, st.active)
+        if k == 0:
+            st.seq_pos.add_(st.active)
+            st.tokens.copy_(st.targets)
+            return
+        # MTP pass 1 over the verify rows: (h_j, target_j) at position p + j
+        mh, mlog = self._mtp(hid, st.targets.view(-1), ctx)
+        am = self.ws.get("dec.am", (T,), torch.int32)
+        C.argmax_lse(mlog, am, None, None)
+        sel = (st.arange_b * kp1 + st.n_acc).long()
+        prev_tok = am[sel]
+        st.drafts[:, 0] = prev_tok
+        h_prev = mh[sel]
+        for j in range(1, k):
+            p2 = st.seq_pos + st.n_acc + j
+            blk2 = st.block_table.gather(1, (p2 // KV_BLOCK).long().view(B, 1)).view(-1)
+            slot2 = blk2.long() * KV_BLOCK + (p2 % KV_BLOCK).long()
+            slot2 = torch.where(st.active.bool(), slot2, torch.full_like(slot2, -1))
+            ctx2 = StepCtx(T=B, pos=p2.int(), seq=st.arange_b, slot=slot2, block_table=st.block_table,
+                           mode="decode", mb=8)
+            h_prev, lg = self._mtp(h_prev, prev_tok, ctx2)
+            dj = self.ws.get("dec.dj", (B,), torch.int32)
+            C.argmax_lse(lg, dj, None, None)
+            st.drafts[:, j] = dj
+            prev_tok = dj
+        C.mtp_finalize(st.targets, st.n_acc, st.drafts, st.tokens, st.seq_pos, st.active)
+
+    def capture(self, st):
+        """Capture decode_body for the state's batch bucket (after one eager warm-up)."""
+        self.decode_body_eager_warm(st)
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
+                self.decode_body(st)
+        torch.cuda.current_stream().wait_stream(s)
+        self.graphs[st.B] = g
+        self.ws_decode.frozen = True
+        return g
+
+    def decode_body_eager_warm(self, st):
+        snap = st.snapshot()
+        self.decode_body(st)
+        st.restore(snap)
+        torch.cuda.synchronize()
+
+
+class DecodeState:
+    """Static device tensors of the decode loop for a bucket of B sequences."""
+
+    def __init__(self, B: int, k: int, max_blocks: int, device):
+        dev = torch.device(device)
+        self.B, self.k = B, k
+        kp1 = k + 1
+        self.tokens = torch.zeros(B, kp1, dtype=torch.int32, device=dev)
+        self.seq_pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.block_table = torch.zeros(B, max_blocks, dtype=torch.int32, device=dev)
+        self.active = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.targets = torch.zeros(B, kp1, dtype=torch.int32, device=dev)
+        self.out_tokens = torch.zeros(B, kp1, dtype=torch.int32, device=dev)
+        self.n_acc = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.drafts = torch.zeros(B, max(k, 1), dtype=torch.int32, device=dev)
+        self.arange_kp1 = torch.arange(kp1, dtype=torch.int32, device=dev)
+        self.arange_b = torch.arange(B, dtype=torch.int32, device=dev)
+        self.seq_rows = torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(kp1)
+        self.active_rows = torch.zeros(B * kp1, dtype=torch.bool, device=dev)
+
+    def set_active(self, mask: torch.Tensor):
+        self.active.copy_(mask.to(self.active.dtype))
+        self.active_rows.copy_(self.active.bool().repeat_interleave(self.k + 1))
+
+    def set_rows(self, rows, first_tokens, positions, drafts):
+        rows_t = torch.tensor(rows, dtype=torch.long, device=self.tokens.device)
+        self.tokens[rows_t, 0] = first_tokens.to(torch.int32)
+        if drafts is not None:
+            self.tokens[rows_t, 1:] = drafts.to(torch.int32)
+        self.seq_pos[rows_t] = positions.to(torch.int32)
+
+    def snapshot(self):
+        return (self.tokens.clone(), self.seq_pos.clone())
+
+    def restore(self, snap):
+        self.tokens.copy_(snap[0])
+        self.seq_pos.copy_(snap[1])

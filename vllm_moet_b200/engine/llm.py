@@ -1,0 +1,245 @@
+"""User-facing engine: ``LLM(model=...).generate(prompts, SamplingParams)``.
+
+One engine object owns the model weights, the paged KV cache, the decode
+state of a batch bucket and (on a GPU) the captured decode graph of that
+bucket.  The loop is: admit waiting requests into free rows (reserve KV
+blocks, batched prefill that also primes the MTP drafts), then replay the
+decode step until some row finishes, refilling freed rows as it goes.  Per
+step the host sends the row-activity vector (pinned H2D) and reads back the
+emitted tokens and acceptance counts (pinned D2H).
+"""
+from __future__ import annotations
+
+import itertools
+import time
+from collections import deque
+from dataclasses import dataclass, field
+from typing import List, Optional, Sequence, Union
+
+import torch
+
+from ..config import EngineConfig, ModelConfig, MoetConfig, ParallelConfig, get_preset
+from ..models.weights import ModelWeights, random_weights
+from .kv_manager import BlockManager
+from .sampling_params import CompletionOutput, RequestOutput, SamplingParams
+from .tokenizer import ByteTokenizer
+
+
+@dataclass
+class _Req:
+    rid: str
+    prompt: List[int]
+    params: SamplingParams
+    out: List[int] = field(default_factory=list)
+    row: int = -1
+    finish: Optional[str] = None
+    t_arrive: float = 0.0
+    t_first: float = 0.0
+    t_done: float = 0.0
+
+
+class LLM:
+    def __init__(self, model: Union[str, ModelConfig] = "tiny-moe", *, device: Optional[str] = None,
+                 num_speculative_tokens: int = 2, max_model_len: int = 4096, max_num_seqs: int = 8,
+                 kv_cache_dtype: str = "bf16", seed: int = 0, weights: Optional[ModelWeights] = None,
+                 num_layers: Optional[int] = None, cuda_graphs: bool = True, num_gpu_blocks: Optional[int] = None,
+                 tensor_parallel_size: int = 1, tp_group=None, tp_rank: int = 0, **model_overrides):
+        cfg = get_preset(model, **model_overrides) if isinstance(model, str) else model
+        if num_layers is not None:
+            cfg = cfg.replace(num_layers=num_layers)
+        if device is None:
+            device = "cuda" if torch.cuda.is_available() else "cpu"
+        self.device = torch.device(device)
+        if self.device.type == "cuda" and cfg.expert_scale != "ue8m0":
+            cfg = cfg.replace(expert_scale="ue8m0")
+        if self.device.type == "cuda" and cfg.dense_dtype != "fp8":
+            cfg = cfg.replace(dense_dtype="fp8")
+        self.cfg = cfg
+        self.ecfg = EngineConfig(model=cfg, moet=MoetConfig.from_env(),
+                                 parallel=ParallelConfig(tp=tensor_parallel_size),
+                                 max_num_seqs=max_num_seqs, max_model_len=max_model_len,
+                                 kv_cache_dtype=kv_cache_dtype, num_speculative_tokens=num_speculative_tokens,
+                                 cuda_graphs=cuda_graphs, seed=seed, device=str(self.device))
+        self.tokenizer = ByteTokenizer(cfg.vocab)
+        self.mw = weights if weights is not None else random_weights(
+            cfg, self.device, seed=seed, tp_rank=tp_rank, tp_size=tensor_parallel_size,
+            with_mtp=num_speculative_tokens > 0)
+        self.k = num_speculative_tokens if self.mw.mtp is not None else 0
+        self.max_blocks = -(-(max_model_len + self.k + 2) // 64)
+        self.stats = {}
+        self._ids = itertools.count()
+        if self.device.type == "cuda":
+            from .gpu_runner import DecodeState, NativeRunner
+            nb = num_gpu_blocks or (max_num_seqs * self.max_blocks + 1)
+            self.blocks = BlockManager(nb)
+            self.runner = NativeRunner(self.mw, self.ecfg, nb, self.device)
+            if tp_group is not None:
+                self.runner.tp_group = tp_group
+            self._DecodeState = DecodeState
+            self._states = {}
+            self._pin_active = None
+        else:
+            from .torch_runner import TorchRunner
+            self.blocks = None
+            self.runner = TorchRunner(self.mw, self.k, max_model_len, self.device)
+
+    # ------------------------------------------------------------------ API
+    def _normalize(self, prompts) -> List[List[int]]:
+        if isinstance(prompts, (str, dict)) or (prompts and isinstance(prompts[0], int)):
+            prompts = [prompts]
+        out = []
+        for p in prompts:
+            if isinstance(p, str):
+                out.append([self.tokenizer.bos_token_id] + self.tokenizer.encode(p))
+            elif isinstance(p, dict):
+                out.append(list(p["prompt_token_ids"]))
+            else:
+                out.append([int(t) for t in p])
+        for p in out:
+            if not p:
+                raise ValueError("empty prompt")
+            if any(t < 0 or t >= self.cfg.vocab for t in p):
+                raise ValueError("prompt token id out of range")
+        return out
+
+    def generate(self, prompts, sampling_params: Union[SamplingParams, Sequence[SamplingParams], None] = None,
+                 use_tqdm: bool = False) -> List[RequestOutput]:
+        toks = self._normalize(prompts)
+        if sampling_params is None:
+            sampling_params = SamplingParams()
+        if isinstance(sampling_params, SamplingParams):
+            sampling_params = [sampling_params] * len(toks)
+        reqs = []
+        for t, sp in zip(toks, sampling_params):
+            if sp.temperature != 0:
+                raise NotImplementedError("this engine serves greedy decoding (temperature 0) on the MTP path")
+            if len(t) + sp.max_tokens + self.k + 1 > self.ecfg.max_model_len:
+                raise ValueError(f"prompt ({len(t)}) + max_tokens ({sp.max_tokens}) exceeds max_model_len")
+            reqs.append(_Req(f"req-{next(self._ids)}", t, sp, t_arrive=time.perf_counter()))
+        if self.device.type == "cuda":
+            self._run_native(reqs)
+        else:
+            self._run_torch(reqs)
+        return [RequestOutput(r.rid, r.prompt, [CompletionOutput(0, self.tokenizer.decode(r.out), r.out,
+                                                                 r.finish)],
+                              metrics=dict(ttft_s=r.t_first - r.t_arrive, e2e_s=r.t_done - r.t_arrive))
+                for r in reqs]
+
+    # ------------------------------------------------------------------ helpers
+    def _emit(self, r: _Req, tokens) -> bool:
+        for t in tokens:
+            if r.finish:
+                break
+            r.out.append(int(t))
+            if not r.params.ignore_eos and (t in r.params.stop_token_ids):
+                r.finish = "stop"
+            elif len(r.out) >= r.params.max_tokens:
+                r.finish = "length"
+        if r.finish and not r.t_done:
+            r.t_done = time.perf_counter()
+        return r.finish is not None
+
+    def _run_torch(self, reqs):
+        waiting = deque(reqs)
+        B = max(1, min(len(reqs), self.ecfg.max_num_seqs))
+        rows = [None] * B
+        steps = accepted = 0
+        while waiting or any(rows):
+            free = [i for i, r in enumerate(rows) if r is None]
+            adm = []
+            while waiting and free:
+                r = waiting.popleft(); r.row = free.pop(0); rows[r.row] = r; adm.append(r)
+            if adm:
+                firsts = self.runner.prefill([r.prompt for r in adm], [r.row for r in adm])
+                for r, f in zip(adm, firsts):
+                    r.t_first = time.perf_counter()
+                    if self._emit(r, [f]):
+                        rows[r.row] = None; self.runner.release(r.row)
+            live = [i for i, r in enumerate(rows) if r is not None]
+            if not live:
+                continue
+            res = self.runner.step(live)
+            steps += 1
+            for i, (toks, a) in res.items():
+                accepted += a
+                if self._emit(rows[i], toks):
+                    self.runner.release(i); rows[i] = None
+        self.stats = dict(steps=steps, accepted=accepted)
+
+    def _state(self, B):
+        st = self._states.get(B)
+        if st is None:
+            st = self._DecodeState(B, self.k, self.max_blocks, self.device)
+            self._states[B] = st
+        return st
+
+    def _run_native(self, reqs):
+        runner = self.runner
+        B = 1
+        while B < min(len(reqs), self.ecfg.max_num_seqs):
+            B *= 2
+        st = self._state(B)
+        kp1 = self.k + 1
+        pin_active = torch.zeros(B, dtype=torch.int32, pin_memory=True)
+        pin_out = torch.zeros(B, kp1, dtype=torch.int32, pin_memory=True)
+        pin_acc = torch.zeros(B, dtype=torch.int32, pin_memory=True)
+        waiting = deque(reqs)
+        rows: List[Optional[_Req]] = [None] * B
+        steps = accepted = 0
+        t_decode = 0.0
+        graph = runner.graphs.get(B) if self.ecfg.cuda_graphs else None
+        bt_host = torch.zeros(B, self.max_blocks, dtype=torch.int32)
+        while waiting or any(r is not None for r in rows):
+            free = [i for i, r in enumerate(rows) if r is None]
+            adm = []
+            while waiting and free and self.blocks.can_allocate(len(waiting[0].prompt) + waiting[0].params.max_tokens + kp1 + 1):
+                r = waiting.popleft()
+                r.row = free.pop(0)
+                rows[r.row] = r
+                blocks = self.blocks.allocate(r.rid, len(r.prompt) + r.params.max_tokens + kp1 + 1)
+                bt_host[r.row].zero_()
+                bt_host[r.row, :len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
+                adm.append(r)
+            if not adm and all(r is None for r in rows):
+                raise MemoryError("KV cache too small for the next request")
+            if adm:
+                st.block_table.copy_(bt_host, non_blocking=False)
+                bts = [bt_host[r.row].tolist() for r in adm]
+                firsts = runner.prefill([r.prompt for r in adm], bts, [r.row for r in adm], st).tolist()
+                now = time.perf_counter()
+                for r, f in zip(adm, firsts):
+                    r.t_first = now
+                    if self._emit(r, [f]):
+                        self._finish_row(r, rows)
+            live = [r is not None for r in rows]
+            if not any(live):
+                continue
+            for i, on in enumerate(live):
+                pin_active[i] = 1 if on else 0
+            st.set_active(pin_active.to(self.device, non_blocking=True))
+            if self.ecfg.cuda_graphs and graph is None:
+                graph = runner.capture(st)
+            t0 = time.perf_counter()
+            if graph is not None:
+                graph.replay()
+            else:
+                runner.decode_body(st)
+            pin_out.copy_(st.out_tokens, non_blocking=True)
+            pin_acc.copy_(st.n_acc, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            t_decode += time.perf_counter() - t0
+            if int(runner.status.item()) != 0:
+                raise RuntimeError(f"device kernel reported status {int(runner.status.item())}")
+            steps += 1
+            for i, r in enumerate(rows):
+                if r is None:
+                    continue
+                a = int(pin_acc[i])
+                accepted += a
+                if self._emit(r, pin_out[i, :a + 1].tolist()):
+                    self._finish_row(r, rows)
+        self.stats = dict(steps=steps, accepted=accepted, decode_s=t_decode, bucket=B)
+
+    def _finish_row(self, r, rows):
+        rows[r.row] = None
+        self.blocks.release(r.rid)

@@ -1,0 +1,81 @@
+"""CPU / reference executor with exactly the native runner's step semantics
+(MTP k-draft verify, greedy acceptance, chained MTP drafts), built on the
+fp32 reference model and per-sequence KV lists.  Used for the CPU engine
+path and as the oracle of the GPU engine."""
+from __future__ import annotations
+
+import torch
+
+from ..models import reference as ref
+from ..models.weights import ModelWeights
+
+
+class TorchRunner:
+    def __init__(self, mw: ModelWeights, k: int, max_len: int, device="cpu"):
+        self.mw = mw
+        self.k = k if mw.mtp is not None else 0
+        self.dev = torch.device(device)
+        self.cs = ref.rope_cos_sin(mw.cfg, max_len + 64, self.dev)
+        self.rows = {}
+
+    def _row(self, r):
+        return self.rows[r]
+
+    @torch.no_grad()
+    def prefill(self, prompts, rows):
+        firsts = []
+        for prompt, r in zip(prompts, rows):
+            n = len(prompt)
+            main, mtp = ref.RefKV(len(self.mw.layers)), ref.RefKV(1)
+            toks = torch.tensor(prompt, device=self.dev)
+            logits, hid = ref.forward(self.mw, toks, torch.arange(n, device=self.dev), self.cs, main)
+            tgt = int(logits[-1].argmax())
+            drafts = []
+            if self.k:
+                nxt = torch.tensor(prompt[1:] + [tgt], device=self.dev)
+                ml, mh = ref.mtp_forward(self.mw, hid, nxt, torch.arange(n, device=self.dev), self.cs, mtp)
+                d = int(ml[-1].argmax()); drafts.append(d)
+                h = mh[-1:]
+                for j in range(1, self.k):
+                    ml, h = ref.mtp_forward(self.mw, h, torch.tensor([d], device=self.dev),
+                                            torch.tensor([n + j - 1], device=self.dev), self.cs, mtp)
+                    d = int(ml[-1].argmax()); drafts.append(d)
+            self.rows[r] = dict(main=main, mtp=mtp, tokens=[tgt] + drafts, pos=n)
+            firsts.append(tgt)
+        return firsts
+
+    @torch.no_grad()
+    def step(self, rows):
+        """-> {row: (emitted tokens list, n_accepted)}"""
+        out = {}
+        k = self.k
+        for r in rows:
+            st = self.rows[r]
+            p = st["pos"]
+            st["main"].truncate(p)
+            toks = torch.tensor(st["tokens"], device=self.dev)
+            pos = torch.arange(p, p + k + 1, device=self.dev)
+            logits, hid = ref.forward(self.mw, toks, pos, self.cs, st["main"])
+            tg = logits.argmax(-1).tolist()
+            a = 0
+            while a < k and st["tokens"][a + 1] == tg[a]:
+                a += 1
+            emitted = tg[: a + 1]
+            drafts = []
+            if k:
+                st["mtp"].truncate(p)
+                ml, mh = ref.mtp_forward(self.mw, hid, torch.tensor(tg, device=self.dev), pos, self.cs, st["mtp"])
+                d = int(ml[a].argmax()); drafts.append(d)
+                h = mh[a:a + 1]
+                st["mtp"].truncate(p + a + 1)
+                for j in range(1, k):
+                    ml, h = ref.mtp_forward(self.mw, h, torch.tensor([d], device=self.dev),
+                                            torch.tensor([p + a + j], device=self.dev), self.cs, st["mtp"])
+                    d = int(ml[-1].argmax()); drafts.append(d)
+            st["tokens"] = [tg[a]] + drafts
+            st["pos"] = p + a + 1
+            out[r] = (emitted, a)
+        return out
+
+    def release(self, r):
+        self.rows.pop(r, None)

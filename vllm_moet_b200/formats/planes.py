@@ -1,0 +1,177 @@
+"""Fragment-major expert planes: the in-memory AND on-disk expert format.
+
+A plane stores one expert weight matrix [N, K] (N output rows, K the
+contraction).  It is cut into 16-row x 64-k blocks ``(nb, kb)``, in that
+order; inside a block each of 32 "lanes" ``(g, t)`` (g = 0..7, t = 0..3)
+owns the elements an m16n8k32 MMA A-fragment needs for two k32 steps:
+
+    rows  g (tile 0) and g + 8 (tile 1)
+    k     kb*64 + k32*32 + half*16 + 4*t + j    (k32, half in {0,1}, j in 0..3)
+
+Byte order within a lane is (tile, k32, half) -> 8 groups of 4 consecutive
+k.  This is the reference layout (P:12015-12039, P:12204-12244,
+P:12113-12186, P:12400-12408); a pack row written by either engine can be
+copied into a GPU slot and served unchanged.
+
+* 2-bit codes: 4 codes per byte, little-endian -> N*K/4 bytes.
+* FP4 (e2m1) nibbles: 2 per byte, low nibble first -> N*K/2 bytes.
+* Quintal refinement: per group of 4 the base-5 number of e2m1 magnitude
+  indices within the code's class (10 bits), 8 words per lane packed into
+  an 80-bit little-endian record; a block stores 32x8 low bytes, then
+  32x2 high bytes -> N*K*5/16 bytes.
+* UE8M0 scales [N, K/32] -> byte at ``(nb*(K/32) + ks)*16 + r``.
+"""
+from __future__ import annotations
+
+import torch
+
+from .codebook import NIBBLE_TO_CODE, dequant_codes
+
+
+def _to_lane_order(x: torch.Tensor) -> torch.Tensor:
+    """[N, K] -> [N/16, K/64, 8(g), 4(t), 2(tile), 2(k32), 2(half), 4(j)] (contiguous)."""
+    N, K = x.shape
+    if N % 16 or K % 64:
+        raise ValueError(f"plane dims must be multiples of (16, 64), got {(N, K)}")
+    # source axes: nb, tile, g, kb, k32, half, t, j
+    v = x.reshape(N // 16, 2, 8, K // 64, 2, 2, 4, 4)
+    return v.permute(0, 3, 2, 6, 1, 4, 5, 7).contiguous()
+
+
+def _from_lane_order(v: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    v = v.reshape(N // 16, K // 64, 8, 4, 2, 2, 2, 4)
+    return v.permute(0, 4, 2, 1, 5, 6, 3, 7).contiguous().reshape(N, K)
+
+
+def pack_codes(codes: torch.Tensor) -> torch.Tensor:
+    """[N, K] u8 codes 0..3 -> plane [N*K/4] u8."""
+    q = _to_lane_order(codes).reshape(-1, 4).to(torch.int32)
+    return (q[:, 0] | (q[:, 1] << 2) | (q[:, 2] << 4) | (q[:, 3] << 6)).to(torch.uint8)
+
+
+def unpack_codes(plane: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    b = plane.reshape(-1, 1).to(torch.int32)
+    q = torch.cat([(b >> s) & 3 for s in (0, 2, 4, 6)], dim=1).to(torch.uint8)
+    return _from_lane_order(q, N, K)
+
+
+def pack_fp4(nibbles: torch.Tensor) -> torch.Tensor:
+    """[N, K] u8 e2m1 nibbles -> plane [N*K/2] u8 (low nibble first)."""
+    q = _to_lane_order(nibbles).reshape(-1, 2).to(torch.int32)
+    return (q[:, 0] | (q[:, 1] << 4)).to(torch.uint8)
+
+
+def unpack_fp4(plane: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    b = plane.reshape(-1, 1)
+    q = torch.cat([b & 0xF, b >> 4], dim=1)
+    return _from_lane_order(q, N, K)
+
+
+def pack_scales(scales: torch.Tensor) -> torch.Tensor:
+    """[N, K/32] u8 -> [N*K/32] u8 with byte (nb, ks, r) at (nb*KS + ks)*16 + r."""
+    N, KS = scales.shape
+    if N % 16:
+        raise ValueError("N must be a multiple of 16")
+    return scales.reshape(N // 16, 16, KS).transpose(1, 2).contiguous().reshape(-1)
+
+
+def unpack_scales(plane: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    KS = K // 32
+    return plane.reshape(N // 16, KS, 16).transpose(1, 2).contiguous().reshape(N, KS)
+
+
+# ---- quintal (radix-5) split-FP4 refinement --------------------------------
+
+_POW5 = (1, 5, 25, 125)
+
+
+def quintal_digits(nibbles: torch.Tensor) -> torch.Tensor:
+    """e2m1 nibbles -> magnitude index within the base code's class (0..4)."""
+    mag = (nibbles & 7).long()
+    code = NIBBLE_TO_CODE.to(nibbles.device)[nibbles.long()]
+    big = (code == 0) | (code == 3)
+    return torch.where(big, mag - 5, mag)
+
+
+def pack_quintal(nibbles: torch.Tensor) -> torch.Tensor:
+    """[N, K] e2m1 nibbles -> quintal plane [N*K*5/16] u8."""
+    N, K = nibbles.shape
+    d = _to_lane_order(quintal_digits(nibbles)).reshape(-1, 8, 4)
+    words = sum(d[..., i] * _POW5[i] for i in range(4))           # [lanes, 8] < 625
+    rec = torch.zeros(words.shape[0], dtype=torch.int64, device=nibbles.device)
+    hi = torch.zeros_like(rec)
+    for w in range(8):                     # 80-bit little-endian record: 64 low + 16 high
+        bit = 10 * w
+        val = words[:, w].long()
+        if bit + 10 <= 64:
+            rec |= val << bit
+        elif bit >= 64:
+            hi |= val << (bit - 64)
+        else:                              # straddles bit 64
+            lo_bits = 64 - bit
+            rec |= (val & ((1 << lo_bits) - 1)) << bit
+            hi |= val >> lo_bits
+    lo_bytes = torch.stack([(rec >> (8 * i)) & 0xFF for i in range(8)], dim=1)
+    hi_bytes = torch.stack([(hi >> (8 * i)) & 0xFF for i in range(2)], dim=1)
+    lo_bytes = lo_bytes.to(torch.uint8).reshape(-1, 32 * 8)
+    hi_bytes = hi_bytes.to(torch.uint8).reshape(-1, 32 * 2)
+    return torch.cat([lo_bytes, hi_bytes], dim=1).reshape(-1)
+
+
+def unpack_quintal_digits(plane: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    blk = plane.reshape(-1, 320)
+    lo = blk[:, :256].reshape(-1, 8).long()
+    hi = blk[:, 256:].reshape(-1, 2).long()
+    rec = sum(lo[:, i] << (8 * i) for i in range(8))
+    hiv = hi[:, 0] | (hi[:, 1] << 8)
+    words = []
+    for w in range(8):
+        bit = 10 * w
+        if bit + 10 <= 64:
+            v = (rec >> bit) & 0x3FF
+        elif bit >= 64:
+            v = (hiv >> (bit - 64)) & 0x3FF
+        else:
+            lo_bits = 64 - bit
+            v = ((rec >> bit) & ((1 << lo_bits) - 1)) | ((hiv << lo_bits) & 0x3FF)
+        words.append(v)
+    words = torch.stack(words, dim=1)                                   # [lanes, 8]
+    digits = torch.stack([(words // p) % 5 for p in _POW5], dim=-1)      # [lanes, 8, 4]
+    return _from_lane_order(digits.to(torch.uint8).reshape(-1), N, K)
+
+
+def quintal_reconstruct(codes: torch.Tensor, digits: torch.Tensor) -> torch.Tensor:
+    """Base codes + quintal digits -> exact e2m1 nibbles."""
+    big = (codes == 0) | (codes == 3)
+    mag = torch.where(big, digits.long() + 5, digits.long())
+    neg = codes <= 1
+    return (mag | (neg.long() << 3)).to(torch.uint8)
+
+
+def div5_magic(x: torch.Tensor) -> torch.Tensor:
+    """x // 5 via (x * 0x334) >> 12, exact for 0 <= x < 1024 (integer identity)."""
+    return (x * 0x334) >> 12
+
+
+# ---- sizes ------------------------------------------------------------------
+
+def codes_plane_bytes(n: int, k: int) -> int:
+    return n * k // 4
+
+
+def scale_plane_bytes(n: int, k: int) -> int:
+    return n * k // 32
+
+
+def fp4_plane_bytes(n: int, k: int) -> int:
+    return n * k // 2
+
+
+def quintal_plane_bytes(n: int, k: int) -> int:
+    if (n * k) % 16:
+        raise ValueError("n*k must be a multiple of 16")
+    return n * k * 5 // 16
+
+
+def dequant_plane(codes_plane: torch.Tensor, scale_plane: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    return dequant_codes(unpack_codes(codes_plane, N, K), unpack_scales(scale_plane, N, K))

@@ -1,0 +1,195 @@
+"""Pure-PyTorch fp32 reference of the MLA + MoE (+ MTP) model.
+
+This is the oracle every native kernel and the whole GPU engine are checked
+against, and the executor of the CPU engine path (BASELINE config 1 runs
+without a GPU).  Weights are used dequantized (FP8 blocks and 2-bit experts
+expanded to fp32); activations stay fp32.  Semantics:
+
+* MLA (DeepSeek-V2/V3 form): q = W_qb RMSNorm(W_qa x), kv = W_kva x split
+  into latent c (RMSNorm) and a shared rope key; k_nope/v = W_kvb c;
+  rotate-half RoPE on the rope dims; softmax scale 1/sqrt(nope + rope).
+* MoE: sigmoid scores + selection bias (optionally group-limited) or
+  softmax; top-k; weights renormalised and scaled; SwiGLU experts with an
+  optional clamp (gate <= L, |up| <= L, DeepSeek-V4 semantics P:6105-6151);
+  shared expert added.
+* MTP: h' = W_eh [RMSNorm(emb(next)); RMSNorm(h)], one decoder layer, head
+  RMSNorm, shared lm_head (DeepSeek-V3 MTP module).
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from ..config import ModelConfig
+from .weights import LayerWeights, ModelWeights
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    x = x.float()
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+
+
+def rope_cos_sin(cfg: ModelConfig, max_pos: int, device="cpu") -> torch.Tensor:
+    """[max_pos, rope] f32 = [cos(half) | sin(half)] for rotate-half RoPE."""
+    half = cfg.qk_rope_dim // 2
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, half, dtype=torch.float64) * 2 / cfg.qk_rope_dim))
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
+    return torch.cat([ang.cos(), ang.sin()], dim=1).float().to(device)
+
+
+def apply_rope(x: torch.Tensor, cs: torch.Tensor) -> torch.Tensor:
+    """x [..., T, rope] with cs [T, rope]."""
+    half = x.shape[-1] // 2
+    c, s = cs[..., :half], cs[..., half:]
+    x1, x2 = x[..., :half], x[..., half:]
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+
+
+def swiglu(gu: torch.Tensor, limit: Optional[float]) -> torch.Tensor:
+    I = gu.shape[-1] // 2
+    g, u = gu[..., :I], gu[..., I:]
+    if limit:
+        g = g.clamp(max=limit)
+        u = u.clamp(-limit, limit)
+    return F.silu(g) * u
+
+
+def route(cfg: ModelConfig, lw: LayerWeights, x: torch.Tensor):
+    """x [T, H] -> (ids [T, k] long, weights [T, k] f32)."""
+    logits = x.float() @ lw.router_w.float().t()
+    if cfg.router == "sigmoid":
+        scores = torch.sigmoid(logits)
+        sel = scores + (lw.router_bias.float() if lw.router_bias is not None else 0.0)
+        if cfg.n_group > 1 and cfg.topk_group < cfg.n_group:
+            T, E = sel.shape
+            gs = sel.view(T, cfg.n_group, E // cfg.n_group)
+            gscore = gs.topk(min(2, E // cfg.n_group), dim=-1).values.sum(-1)
+            keep = torch.zeros_like(gscore, dtype=torch.bool)
+            keep.scatter_(1, _stable_topk(gscore, cfg.topk_group), True)
+            sel = sel.masked_fill(~keep.repeat_interleave(E // cfg.n_group, dim=1), float("-inf"))
+    else:
+        scores = torch.softmax(logits, dim=-1)
+        sel = scores
+    ids = _stable_topk(sel, cfg.top_k)
+    w = scores.gather(1, ids)
+    if cfg.norm_topk_prob:
+        w = w / (w.sum(-1, keepdim=True) + 1e-20)
+    return ids, w * cfg.routed_scaling
+
+
+def _stable_topk(x: torch.Tensor, k: int) -> torch.Tensor:
+    """Top-k indices, ties broken toward the lower index (matches the kernel)."""
+    # stable sort on -value keeps index order among ties
+    _, perm = torch.sort(-x, dim=1, stable=True)
+    return perm[:, :k]
+
+
+def moe_block(cfg: ModelConfig, lw: LayerWeights, h: torch.Tensor) -> torch.Tensor:
+    ids, w = route(cfg, lw, h)
+    out = torch.zeros_like(h, dtype=torch.float32)
+    for e in torch.unique(ids).tolist():
+        rows, slot = (ids == e).nonzero(as_tuple=True)
+        w13, w2 = lw.experts.dequant_expert(e)
+        y = swiglu(h[rows].float() @ w13.float().t(), cfg.swiglu_limit) @ w2.float().t()
+        out.index_add_(0, rows, y * w[rows, slot, None])
+    if lw.shared_gate_up is not None:
+        out = out + swiglu(h.float() @ lw.shared_gate_up.dequant().t(), cfg.swiglu_limit) @ lw.shared_down.dequant().t()
+    return out
+
+
+def dense_ffn(cfg: ModelConfig, lw: LayerWeights, h: torch.Tensor) -> torch.Tensor:
+    return swiglu(h.float() @ lw.gate_up.dequant().t(), None) @ lw.down.dequant().t()
+
+
+class RefKV:
+    """Per-sequence, per-layer cache of (k [Hh, L, qk], v [Hh, L, v]) in fp32."""
+
+    def __init__(self, n_layers: int):
+        self.k = [None] * n_layers
+        self.v = [None] * n_layers
+
+    def truncate(self, length: int):
+        for i in range(len(self.k)):
+            if self.k[i] is not None:
+                self.k[i] = self.k[i][:, :length]
+                self.v[i] = self.v[i][:, :length]
+
+
+def attention(cfg: ModelConfig, lw: LayerWeights, x: torch.Tensor, positions: torch.Tensor, cs: torch.Tensor,
+              cache: Optional[RefKV] = None, li: int = 0, heads: Optional[int] = None) -> torch.Tensor:
+    """x [T, H] (normed), positions [T] (contiguous, appended after the cache) -> [T, H]."""
+    Hh = heads or cfg.num_heads
+    T = x.shape[0]
+    nope, rope, vd, lat = cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim, cfg.kv_lora_rank
+    qkva = x.float() @ lw.qkv_a.dequant().t()
+    qa = rms_norm(qkva[:, : cfg.q_lora_rank], lw.q_a_norm, cfg.rms_eps)
+    c = rms_norm(qkva[:, cfg.q_lora_rank: cfg.q_lora_rank + lat], lw.kv_a_norm, cfg.rms_eps)
+    kr = qkva[:, cfg.q_lora_rank + lat:]
+    q = (qa @ lw.q_b.dequant().t()).view(T, Hh, nope + rope)
+    pcs = cs[positions]
+    q_nope, q_pe = q[..., :nope], apply_rope(q[..., nope:].transpose(0, 1), pcs).transpose(0, 1)
+    kr = apply_rope(kr, pcs)
+    kvb = (c @ lw.kv_b.dequant().t()).view(T, Hh, nope + vd)
+    k = torch.cat([kvb[..., :nope], kr[:, None, :].expand(T, Hh, rope)], dim=-1).transpose(0, 1)  # [Hh,T,qk]
+    v = kvb[..., nope:].transpose(0, 1)
+    qf = torch.cat([q_nope, q_pe], dim=-1).transpose(0, 1)  # [Hh, T, qk]
+    if cache is not None:
+        if cache.k[li] is not None:
+            k = torch.cat([cache.k[li], k], dim=1)
+            v = torch.cat([cache.v[li], v], dim=1)
+        cache.k[li], cache.v[li] = k, v
+    L = k.shape[1]
+    scale = 1.0 / math.sqrt(nope + rope)
+    s = (qf @ k.transpose(1, 2)) * scale                   # [Hh, T, L]
+    kpos = torch.arange(L, device=x.device)
+    qpos = (L - T) + torch.arange(T, device=x.device)
+    s = s.masked_fill(kpos[None, None, :] > qpos[None, :, None], float("-inf"))
+    o = torch.softmax(s, dim=-1) @ v                       # [Hh, T, vd]
+    return o.transpose(0, 1).reshape(T, Hh * vd) @ lw.o.dequant().t()
+
+
+def decoder_layer(cfg, lw, x, positions, cs, cache=None, li=0):
+    h = rms_norm(x, lw.attn_norm, cfg.rms_eps)
+    x = x + attention(cfg, lw, h, positions, cs, cache, li)
+    h = rms_norm(x, lw.ffn_norm, cfg.rms_eps)
+    return x + (moe_block(cfg, lw, h) if lw.is_moe else dense_ffn(cfg, lw, h))
+
+
+def forward(mw: ModelWeights, tokens: torch.Tensor, positions: torch.Tensor, cs: torch.Tensor,
+            cache: Optional[RefKV] = None):
+    """-> (logits [T, V] f32, final normed hidden [T, H] f32)."""
+    cfg = mw.cfg
+    x = mw.embed[tokens].float()
+    for li, lw in enumerate(mw.layers):
+        x = decoder_layer(cfg, lw, x, positions, cs, cache, li)
+    h = rms_norm(x, mw.final_norm, cfg.rms_eps)
+    return h @ mw.lm_head.dequant().t(), h
+
+
+def mtp_forward(mw: ModelWeights, hidden: torch.Tensor, next_tokens: torch.Tensor, positions: torch.Tensor,
+                cs: torch.Tensor, cache: Optional[RefKV] = None):
+    """MTP module: (h_i, token_{i+1}) at position i -> logits for token_{i+2}; returns (logits, hidden)."""
+    cfg, m = mw.cfg, mw.mtp
+    e = rms_norm(mw.embed[next_tokens].float(), m.enorm, cfg.rms_eps)
+    hn = rms_norm(hidden, m.hnorm, cfg.rms_eps)
+    x = torch.cat([e, hn], dim=-1) @ m.eh_proj.dequant().t()
+    x = decoder_layer(cfg, m.layer, x, positions, cs, cache, 0)
+    h = rms_norm(x, m.head_norm, cfg.rms_eps)
+    return h @ mw.lm_head.dequant().t(), h
+
+
+def greedy_generate(mw: ModelWeights, prompt: list, max_tokens: int) -> list:
+    """Full-recompute greedy decoding (no cache): the end-to-end oracle."""
+    cs = rope_cos_sin(mw.cfg, len(prompt) + max_tokens + 8, device=mw.embed.device)
+    toks = list(prompt)
+    out = []
+    for _ in range(max_tokens):
+        t = torch.tensor(toks, device=mw.embed.device)
+        logits, _ = forward(mw, t, torch.arange(len(toks), device=t.device), cs)
+        nxt = int(logits[-1].argmax())
+        out.append(nxt)
+        toks.append(nxt)
+    return out

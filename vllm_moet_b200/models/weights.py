@@ -1,0 +1,342 @@
+"""Model weights: containers, expert slot layout, and synthetic random init.
+
+Dense stack: FP8 e4m3 with UE8M0 128x128 block scales (:class:`Fp8Linear`),
+or plain float for the CPU tiny model.  Routed experts: one slot per expert
+holding ``[codes13 | sc13 | codes2 | sc2]`` -- the fragment-major 2-bit
+planes of the fused gate/up matrix [2I, H] and of the down matrix [H, I]
+with their UE8M0 scale planes (the pack-row section order of the
+reference's base tier, P:12830-12869).  A layer's experts live in one pool
+tensor [E, slot_bytes] addressed through an expert -> slot table, so the
+residency tiers can swap the pool for a cache without touching kernels.
+
+Random init follows the benchmark configs: N(0, 0.02) weights; experts go
+through NVFP4 (e2m1 + e4m3 block-16 + f32 tensor scale) and are then
+re-quantised to the 2-bit codebook (GPU kernels on CUDA, the golden torch
+pipeline on CPU).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+
+from ..config import ModelConfig
+from ..formats import codebook, fp8, planes
+
+
+# --------------------------------------------------------------------------
+@dataclass
+class Fp8Linear:
+    """y = x W^T with W [N, K] in e4m3 (uint8 storage) + UE8M0 [ceil(N/128), ceil(K/128)]."""
+    w: torch.Tensor
+    s: torch.Tensor
+
+    @property
+    def shape(self):
+        return tuple(self.w.shape)
+
+    @classmethod
+    def from_float(cls, w: torch.Tensor) -> "Fp8Linear":
+        q, s = fp8.quant_weight_fp8(w)
+        return cls(q.view(torch.uint8), s)
+
+    def dequant(self) -> torch.Tensor:
+        return fp8.dequant_weight_fp8(self.w.view(torch.float8_e4m3fn), self.s)
+
+    def to(self, device) -> "Fp8Linear":
+        return Fp8Linear(self.w.to(device), self.s.to(device))
+
+
+@dataclass
+class FloatLinear:
+    w: torch.Tensor
+
+    @property
+    def shape(self):
+        return tuple(self.w.shape)
+
+    def dequant(self) -> torch.Tensor:
+        return self.w.float()
+
+    def to(self, device) -> "FloatLinear":
+        return FloatLinear(self.w.to(device))
+
+
+def make_linear(w: torch.Tensor, dtype: str):
+    if dtype == "fp8":
+        return Fp8Linear.from_float(w)
+    return FloatLinear(w.float())
+
+
+# --------------------------------------------------------------------------
+@dataclass
+class ExpertLayout:
+    """Byte layout of one expert slot [codes13 | sc13 | codes2 | sc2]."""
+    H: int
+    I: int
+
+    @property
+    def codes13(self) -> int:
+        return planes.codes_plane_bytes(2 * self.I, self.H)
+
+    @property
+    def sc13(self) -> int:
+        return planes.scale_plane_bytes(2 * self.I, self.H)
+
+    @property
+    def codes2(self) -> int:
+        return planes.codes_plane_bytes(self.H, self.I)
+
+    @property
+    def sc2(self) -> int:
+        return planes.scale_plane_bytes(self.H, self.I)
+
+    @property
+    def off_codes13(self) -> int:
+        return 0
+
+    @property
+    def off_sc13(self) -> int:
+        return self.codes13
+
+    @property
+    def off_codes2(self) -> int:
+        return self.codes13 + self.sc13
+
+    @property
+    def off_sc2(self) -> int:
+        return self.codes13 + self.sc13 + self.codes2
+
+    @property
+    def slot_bytes(self) -> int:
+        return self.codes13 + self.sc13 + self.codes2 + self.sc2
+
+    def split(self, slot: torch.Tensor):
+        o = [0, self.codes13, self.sc13, self.codes2, self.sc2]
+        c = [sum(o[: i + 1]) for i in range(5)]
+        return tuple(slot[..., c[i]:c[i + 1]] for i in range(4))
+
+
+@dataclass
+class ExpertPool:
+    """All routed experts of one layer: pool [E, slot_bytes] + slot table [E]."""
+    layout: ExpertLayout
+    pool: torch.Tensor
+    slot_table: torch.Tensor
+    # CPU tiny config with fp16 group scales keeps dequantized matrices instead
+    dense_w13: Optional[torch.Tensor] = None
+    dense_w2: Optional[torch.Tensor] = None
+
+    def dequant_expert(self, e: int):
+        """-> (w13 [2I, H], w2 [H, I]) float32."""
+        if self.dense_w13 is not None:
+            return self.dense_w13[e], self.dense_w2[e]
+        L = self.layout
+        c13, s13, c2, s2 = L.split(self.pool[int(self.slot_table[e])])
+        w13 = planes.dequant_plane(c13.cpu(), s13.cpu(), 2 * L.I, L.H)
+        w2 = planes.dequant_plane(c2.cpu(), s2.cpu(), L.H, L.I)
+        return w13.to(self.pool.device), w2.to(self.pool.device)
+
+
+@dataclass
+class LayerWeights:
+    attn_norm: torch.Tensor
+    qkv_a: object                  # [q_lora + kv_lora + rope, H]
+    q_a_norm: torch.Tensor
+    kv_a_norm: torch.Tensor
+    q_b: object                    # [Hh*(nope+rope), q_lora]
+    kv_b: object                   # [Hh*(nope+v), kv_lora]
+    o: object                      # [H, Hh*v]
+    ffn_norm: torch.Tensor
+    # dense FFN
+    gate_up: object = None         # [2I, H]
+    down: object = None            # [H, I]
+    # MoE
+    router_w: Optional[torch.Tensor] = None     # [E, H] f32
+    router_bias: Optional[torch.Tensor] = None  # [E] f32
+    experts: Optional[ExpertPool] = None
+    shared_gate_up: object = None
+    shared_down: object = None
+    # absorbed MLA decode weights (derived from kv_b)
+    w_uk_t: Optional[Fp8Linear] = None          # [Hh, kv_lora, nope]
+    w_uv: Optional[Fp8Linear] = None            # [Hh, v, kv_lora]
+    # sparse indexer (GLM shape)
+    idx_wq: object = None
+    idx_wk: object = None
+
+    @property
+    def is_moe(self) -> bool:
+        return self.experts is not None
+
+
+@dataclass
+class MTPWeights:
+    enorm: torch.Tensor
+    hnorm: torch.Tensor
+    eh_proj: object                # [H, 2H]
+    layer: LayerWeights
+    head_norm: torch.Tensor
+
+
+@dataclass
+class ModelWeights:
+    cfg: ModelConfig
+    embed: torch.Tensor            # [V, H] bf16
+    layers: list
+    final_norm: torch.Tensor
+    lm_head: object                # [V, H]
+    mtp: Optional[MTPWeights] = None
+    tp_rank: int = 0
+    tp_size: int = 1
+    extra: dict = field(default_factory=dict)
+
+
+# --------------------------------------------------------------------------
+def _derive_absorb(kv_b, cfg: ModelConfig, heads: int):
+    """kv_b [Hh*(nope+v), kv_lora] -> W_uk^T [Hh, kv_lora, nope], W_uv [Hh, v, kv_lora] (FP8)."""
+    w = kv_b.dequant().view(heads, cfg.qk_nope_dim + cfg.v_head_dim, cfg.kv_lora_rank)
+    wuk_t = w[:, : cfg.qk_nope_dim, :].transpose(1, 2).contiguous()        # [Hh, 512, nope]
+    wuv = w[:, cfg.qk_nope_dim:, :].contiguous()                           # [Hh, v, 512]
+    qs = [Fp8Linear.from_float(wuk_t[h]) for h in range(heads)]
+    vs = [Fp8Linear.from_float(wuv[h]) for h in range(heads)]
+    return (Fp8Linear(torch.stack([q.w for q in qs]), torch.stack([q.s for q in qs])),
+            Fp8Linear(torch.stack([v.w for v in vs]), torch.stack([v.s for v in vs])))
+
+
+class _Rng:
+    """Deterministic normal generator on a device (seeded per named tensor)."""
+
+    def __init__(self, seed: int, device):
+        self.seed = seed
+        self.device = torch.device(device)
+        self.gen = torch.Generator(device=self.device)
+        self.counter = 0
+
+    def normal(self, shape, std=0.02):
+        self.counter += 1
+        self.gen.manual_seed(self.seed * 1000003 + self.counter)
+        return torch.randn(shape, generator=self.gen, device=self.device, dtype=torch.float32) * std
+
+
+def quantize_experts_gpu(w13: torch.Tensor, w2: torch.Tensor, layout: ExpertLayout, out_pool: torch.Tensor,
+                         zero_mode: str = "auto"):
+    """Random-init float experts [n, 2I, H], [n, H, I] (cuda) -> 2-bit slots in out_pool [n, slot_bytes]
+    via NVFP4 (kernel) then the 2-bit requant+pack kernel."""
+    from ..ops import native
+    C = native()
+    n = w13.shape[0]
+    for e in range(n):
+        for (mat, off_c, off_s) in ((w13[e], layout.off_codes13, layout.off_sc13),
+                                    (w2[e], layout.off_codes2, layout.off_sc2)):
+            N, K = mat.shape
+            ts = float(mat.abs().max()) / (6.0 * 448.0) or 1.0
+            packed = torch.empty(N, K // 2, dtype=torch.uint8, device=mat.device)
+            sf = torch.empty(N, K // 16, dtype=torch.uint8, device=mat.device)
+            C.nvfp4_quant(mat.contiguous(), ts, packed, sf)
+            nc, ns = N * K // 4, N * K // 32
+            counters = torch.zeros(2, dtype=torch.int64, device=mat.device)
+            mode = 1 if zero_mode == "alt" else 0
+            C.w2_quant_pack(packed, sf, ts, mode, out_pool[e, off_c:off_c + nc], out_pool[e, off_s:off_s + ns],
+                            None, counters)
+            if zero_mode == "auto":
+                nz, nneg = (int(v) for v in counters.tolist())
+                if nz and min(nneg, nz - nneg) < 0.05 * nz:
+                    C.w2_quant_pack(packed, sf, ts, 1, out_pool[e, off_c:off_c + nc],
+                                    out_pool[e, off_s:off_s + ns], None, None)
+
+
+def quantize_experts_cpu(w13: torch.Tensor, w2: torch.Tensor, layout: ExpertLayout, out_pool: torch.Tensor,
+                         zero_mode: str = "auto"):
+    """Golden torch pipeline (NVFP4 -> f64 -> 2-bit) for CPU / tests."""
+    for e in range(w13.shape[0]):
+        for (mat, off_c, off_s) in ((w13[e], layout.off_codes13, layout.off_sc13),
+                                    (w2[e], layout.off_codes2, layout.off_sc2)):
+            N, K = mat.shape
+            ts = float(mat.abs().max()) / (6.0 * 448.0) or 1.0
+            packed, sf, t2 = codebook.f32_to_nvfp4(mat.float().cpu(), ts)
+            codes, sc, _ = codebook.nvfp4_to_codes_scales(packed, sf, t2, mode=zero_mode)
+            out_pool[e, off_c:off_c + N * K // 4] = planes.pack_codes(codes).to(out_pool.device)
+            out_pool[e, off_s:off_s + N * K // 32] = planes.pack_scales(sc).to(out_pool.device)
+
+
+def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0, tp_size=1,
+                expert_chunk: int = 16) -> LayerWeights:
+    H, dt = cfg.hidden, cfg.dense_dtype
+    Hh = cfg.num_heads // tp_size
+    qk = cfg.qk_head_dim
+    lin = lambda shape: make_linear(rng.normal(shape), dt)  # noqa: E731
+    ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=dev)  # noqa: E731
+    q_lora = cfg.q_lora_rank
+    lw = LayerWeights(
+        attn_norm=ones(H),
+        qkv_a=lin((q_lora + cfg.kv_lora_rank + cfg.qk_rope_dim, H)),
+        q_a_norm=ones(q_lora),
+        kv_a_norm=ones(cfg.kv_lora_rank),
+        q_b=lin((Hh * qk, q_lora)),
+        kv_b=lin((Hh * (cfg.qk_nope_dim + cfg.v_head_dim), cfg.kv_lora_rank)),
+        o=lin((H, Hh * cfg.v_head_dim)),
+        ffn_norm=ones(H),
+    )
+    if isinstance(lw.kv_b, Fp8Linear):
+        lw.w_uk_t, lw.w_uv = _derive_absorb(lw.kv_b, cfg, Hh)
+    if not moe:
+        I = cfg.dense_intermediate // tp_size
+        lw.gate_up = lin((2 * I, H))
+        lw.down = lin((H, I))
+        return lw
+    E, I = cfg.num_experts, cfg.moe_intermediate // tp_size
+    lw.router_w = rng.normal((E, H))
+    lw.router_bias = torch.zeros(E, dtype=torch.float32, device=dev)
+    Is = cfg.moe_intermediate * cfg.num_shared_experts // tp_size
+    if cfg.num_shared_experts:
+        lw.shared_gate_up = lin((2 * Is, H))
+        lw.shared_down = lin((H, Is))
+    layout = ExpertLayout(H=H, I=I)
+    if cfg.expert_scale == "fp16_amax4":
+        # CPU tiny config: fp16 group-32 scale = max|w|/4; keep the dequantized experts
+        w13s, w2s = [], []
+        for e in range(E):
+            a = rng.normal((2 * I, H)); b = rng.normal((H, I))
+            c, s = codebook.f32_to_codes_fp16_amax4(a); w13s.append(codebook.dequant_codes_fp16(c, s))
+            c, s = codebook.f32_to_codes_fp16_amax4(b); w2s.append(codebook.dequant_codes_fp16(c, s))
+        pool = torch.zeros(E, 16, dtype=torch.uint8, device=dev)
+        lw.experts = ExpertPool(layout, pool, torch.arange(E, dtype=torch.int32, device=dev),
+                                dense_w13=torch.stack(w13s), dense_w2=torch.stack(w2s))
+        return lw
+    pool = torch.empty(E, layout.slot_bytes, dtype=torch.uint8, device=dev)
+    for e0 in range(0, E, expert_chunk):
+        n = min(expert_chunk, E - e0)
+        w13 = rng.normal((n, 2 * I, H))
+        w2 = rng.normal((n, H, I))
+        if torch.device(dev).type == "cuda":
+            quantize_experts_gpu(w13, w2, layout, pool[e0:e0 + n])
+        else:
+            quantize_experts_cpu(w13, w2, layout, pool[e0:e0 + n])
+        del w13, w2
+    lw.experts = ExpertPool(layout, pool, torch.arange(E, dtype=torch.int32, device=dev))
+    return lw
+
+
+def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int = 0, tp_size: int = 1,
+                   with_mtp: bool = True, num_layers: Optional[int] = None) -> ModelWeights:
+    """Synthetic random-init weights of the given architecture (N(0, 0.02))."""
+    dev = torch.device(device)
+    rng = _Rng(seed, dev)
+    H = cfg.hidden
+    L = cfg.num_layers if num_layers is None else num_layers
+    embed = rng.normal((cfg.vocab, H)).to(torch.bfloat16)
+    layers = [_make_layer(cfg, rng, i, dev, cfg.is_moe_layer(i), tp_rank, tp_size) for i in range(L)]
+    mw = ModelWeights(cfg=cfg, embed=embed, layers=layers,
+                      final_norm=torch.ones(H, dtype=torch.bfloat16, device=dev),
+                      lm_head=make_linear(rng.normal((cfg.vocab, H)), cfg.dense_dtype),
+                      tp_rank=tp_rank, tp_size=tp_size)
+    if with_mtp and cfg.num_mtp_layers:
+        mw.mtp = MTPWeights(
+            enorm=torch.ones(H, dtype=torch.bfloat16, device=dev),
+            hnorm=torch.ones(H, dtype=torch.bfloat16, device=dev),
+            eh_proj=make_linear(rng.normal((H, 2 * H)), cfg.dense_dtype),
+            layer=_make_layer(cfg, rng, L, dev, True, tp_rank, tp_size),
+            head_norm=torch.ones(H, dtype=torch.bfloat16, device=dev))
+    return mw
