@@ -1,0 +1,57 @@
+"""CPU engine: BASELINE config 1 (tiny MoE) end to end, config validation."""
+import pytest
+import torch
+
+from vllm_moet_b200 import SamplingParams
+from vllm_moet_b200.config import EngineConfig, MoetConfig, ParallelConfig, tiny_config
+from vllm_moet_b200.engine.llm import LLM
+from vllm_moet_b200.models import reference
+
+
+@pytest.fixture(scope="module")
+def tiny_llm():
+    return LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+
+
+def test_tiny_mtp_engine_matches_full_recompute(tiny_llm):
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(3, 1024, (32,), generator=g).tolist() for _ in range(4)]
+    outs = tiny_llm.generate(prompts, SamplingParams(max_tokens=16, ignore_eos=True))
+    for p, o in zip(prompts, outs):
+        assert o.outputs[0].token_ids == reference.greedy_generate(tiny_llm.mw, p, 16)
+
+
+def test_tiny_engine_without_mtp():
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=0, max_model_len=128)
+    p = [5, 6, 7, 8]
+    o = llm.generate([p], SamplingParams(max_tokens=6, ignore_eos=True))
+    assert o[0].outputs[0].token_ids == reference.greedy_generate(llm.mw, p, 6)
+
+
+def test_string_prompt_and_stop_token(tiny_llm):
+    o = tiny_llm.generate("hello", SamplingParams(max_tokens=5))
+    assert 1 <= len(o[0].outputs[0].token_ids) <= 5
+    first = o[0].outputs[0].token_ids[0]
+    o2 = tiny_llm.generate("hello", SamplingParams(max_tokens=5, stop_token_ids=[first]))
+    assert o2[0].outputs[0].token_ids == [first] and o2[0].outputs[0].finish_reason == "stop"
+
+
+def test_config_validation():
+    with pytest.raises(ValueError, match="ZERO_MODE"):
+        MoetConfig(zero_mode="typo")
+    with pytest.raises(ValueError, match="gate"):
+        MoetConfig(gate=True)
+    with pytest.raises(ValueError):
+        ParallelConfig(tp=3)
+    with pytest.raises(ValueError, match="nvfp4"):
+        EngineConfig(model=tiny_config(), kv_cache_dtype="nvfp4")
+    with pytest.raises(ValueError):
+        SamplingParams(max_tokens=0)
+
+
+def test_env_aliases(monkeypatch):
+    monkeypatch.setenv("VLLM_MOE_W2_PREFILL_T", "128")
+    monkeypatch.setenv("VLLM_MOE_W2_DELTA", "1")
+    monkeypatch.setenv("VLLM_MOE_W2_GATE_TAU", "0.7")
+    c = MoetConfig.from_env()
+    assert c.prefill_t == 128 and c.delta is True and c.gate_tau == 0.7

@@ -1,0 +1,358 @@
+"""Numerics of every native kernel against a plain PyTorch fp32/fp64 reference."""
+import math
+
+import pytest
+import torch
+
+from vllm_moet_b200.formats import codebook, fp8, kv_nvfp4, planes
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def C():
+    from vllm_moet_b200.ops import native
+    return native()
+
+
+def rel(a, b):
+    a, b = a.double(), b.double()
+    return float((a - b).norm() / (b.norm() + 1e-30))
+
+
+def rand_e4m3(shape, g):
+    x = torch.randn(shape, generator=g) * 2
+    return x.clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
+
+
+# ------------------------------------------------------------------------- quantisation
+@pytest.mark.parametrize("T,H", [(1, 512), (5, 4096), (33, 1024)])
+def test_rmsnorm_quant(C, T, H):
+    g = torch.Generator().manual_seed(T)
+    x = (torch.randn(T, H, generator=g) * 3).to(torch.bfloat16)
+    add = (torch.randn(T, H, generator=g)).to(torch.bfloat16)
+    w = (torch.rand(H, generator=g) + 0.5).to(torch.bfloat16)
+    xd, ad, wd = x.to(DEV), add.to(DEV), w.to(DEV)
+    xo = torch.empty_like(xd)
+    y = torch.empty_like(xd)
+    q0 = torch.empty(T, H, dtype=torch.uint8, device=DEV); s0 = torch.empty(T, H // 64, dtype=torch.uint8, device=DEV)
+    q1 = torch.empty_like(q0); s1 = torch.empty_like(s0)
+    C.rmsnorm_quant(xd, ad, xo, wd, 1e-6, y, q0, s0, q1, s1, 0)
+    xs = (x.float() + add.float()).to(torch.bfloat16)
+    assert torch.equal(xo.cpu(), xs)
+    ref = (xs.float() * torch.rsqrt(xs.float().pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()).to(torch.bfloat16)
+    assert rel(y.cpu().float(), ref.float()) < 1e-2
+    rq, rs = fp8.quant_act_fp8(y.cpu().float())
+    assert (s0.cpu() == rs).float().mean() > 0.99
+    deq = fp8.dequant_act_fp8(q0.cpu().view(torch.float8_e4m3fn), s0.cpu())
+    assert rel(deq, y.cpu().float()) < 4e-2
+    # w2 layout is the natural bytes permuted inside 32-blocks
+    assert torch.equal(q1.cpu(), fp8.to_w2_layout(q0.cpu()))
+    assert torch.equal(s1.cpu(), s0.cpu())
+
+
+def test_swiglu_quant(C):
+    g = torch.Generator().manual_seed(0)
+    R, I = 7, 256
+    x = torch.randn(R, 2 * I, generator=g) * 8
+    q = torch.empty(R, I, dtype=torch.uint8, device=DEV); s = torch.empty(R, I // 64, dtype=torch.uint8, device=DEV)
+    C.swiglu_quant(x.to(DEV), 10.0, None, 0, q, s)
+    gt, up = x[:, :I].clamp(max=10), x[:, I:].clamp(-10, 10)
+    ref = (torch.nn.functional.silu(gt) * up).to(torch.bfloat16).float()
+    deq = fp8.dequant_act_fp8(q.cpu().view(torch.float8_e4m3fn), s.cpu())
+    assert rel(deq, ref) < 4e-2
+
+
+# ------------------------------------------------------------------------- dense FP8 GEMV
+@pytest.mark.parametrize("T,N,K", [(1, 1600, 4096), (3, 96, 512), (13, 256, 1024), (40, 4096, 128), (96, 130, 192)])
+def test_gemv_fp8(C, T, N, K):
+    g = torch.Generator().manual_seed(N + T)
+    a = rand_e4m3((T, K), g)
+    sa = torch.randint(120, 134, (T, K // 64), generator=g, dtype=torch.uint8)
+    w = rand_e4m3((N, K), g)
+    sw = torch.randint(118, 130, ((N + 127) // 128, (K + 127) // 128), generator=g, dtype=torch.uint8)
+    out = torch.empty(T, N, dtype=torch.float32, device=DEV)
+    C.gemv_fp8(a.to(DEV), sa.to(DEV), w.to(DEV), sw.to(DEV), out, None)
+    A = fp8.dequant_act_fp8(a.view(torch.float8_e4m3fn), sa).double()
+    Wd = w.view(torch.float8_e4m3fn).double() * torch.exp2(sw.double() - 127).repeat_interleave(128, 0)[:N].repeat_interleave(128, 1)[:, :K]
+    ref = A @ Wd.t()
+    assert rel(out.cpu(), ref) < 1e-4
+    # bf16 output + residual
+    res = torch.randn(T, N, generator=g).to(torch.bfloat16)
+    outb = torch.empty(T, N, dtype=torch.bfloat16, device=DEV)
+    C.gemv_fp8(a.to(DEV), sa.to(DEV), w.to(DEV), sw.to(DEV), outb, res.to(DEV))
+    assert rel(outb.cpu().float(), ref.float() + res.float()) < 1e-2
+
+
+def test_gemv_fp8_batched(C):
+    g = torch.Generator().manual_seed(7)
+    B, T, N, K = 4, 3, 512, 128
+    a = rand_e4m3((T, B, K), g)                   # [T, B, K] viewed as [B, T, K]
+    sa = torch.randint(120, 134, (T, B, K // 64), generator=g, dtype=torch.uint8)
+    w = rand_e4m3((B, N, K), g)
+    sw = torch.randint(118, 130, (B, N // 128, 1), generator=g, dtype=torch.uint8)
+    out = torch.zeros(T, B, N + 64, dtype=torch.bfloat16, device=DEV)
+    C.gemv_fp8(a.to(DEV).permute(1, 0, 2), sa.to(DEV).permute(1, 0, 2), w.to(DEV), sw.to(DEV),
+               out[:, :, :N].permute(1, 0, 2), None)
+    for b in range(B):
+        A = fp8.dequant_act_fp8(a[:, b].view(torch.float8_e4m3fn), sa[:, b]).double()
+        Wd = w[b].view(torch.float8_e4m3fn).double() * torch.exp2(sw[b].double() - 127).repeat_interleave(128, 0).repeat_interleave(128, 1)
+        assert rel(out[:, b, :N].cpu().float(), (A @ Wd.t()).float()) < 1e-2
+    assert (out[:, :, N:] == 0).all()
+
+
+# ------------------------------------------------------------------------- routing + 2-bit experts
+def test_router_topk_matches_reference(C):
+    from types import SimpleNamespace
+    from vllm_moet_b200.config import ds4_flash_config
+    from vllm_moet_b200.models.reference import route
+    cfg = ds4_flash_config(n_group=8, topk_group=4)
+    g = torch.Generator().manual_seed(0)
+    T, E, H = 17, 256, 64
+    x = torch.randn(T, H, generator=g)
+    lw = SimpleNamespace(router_w=torch.randn(E, H, generator=g), router_bias=torch.randn(E, generator=g) * 0.1)
+    ids_ref, w_ref = route(cfg, lw, x)
+    logits = (x @ lw.router_w.t()).to(DEV)
+    ids = torch.empty(T, 8, dtype=torch.int32, device=DEV); w = torch.empty(T, 8, device=DEV)
+    C.router_topk(logits, lw.router_bias.to(DEV), 8, True, 8, 4, True, cfg.routed_scaling, ids, w)
+    assert torch.equal(ids.cpu().long(), ids_ref)
+    assert rel(w.cpu(), w_ref) < 1e-5
+    # softmax router, no groups
+    cfg2 = ds4_flash_config(router="softmax", norm_topk_prob=False, routed_scaling=1.0)
+    ids_ref, w_ref = route(cfg2, lw, x)
+    C.router_topk(logits, None, 8, False, 1, 1, False, 1.0, ids, w)
+    assert torch.equal(ids.cpu().long(), ids_ref)
+    assert rel(w.cpu(), w_ref) < 1e-5
+
+
+def _expert_pool(E, N, K, g, lo=122, hi=130):
+    codes = torch.randint(0, 4, (E, N, K), generator=g, dtype=torch.uint8)
+    sc = torch.randint(lo, hi, (E, N, K // 32), generator=g, dtype=torch.uint8)
+    pool = torch.stack([torch.cat([planes.pack_codes(codes[e]), planes.pack_scales(sc[e])]) for e in range(E)])
+    return codes, sc, pool
+
+
+@pytest.mark.parametrize("T,k,E,N,K,MB", [(1, 8, 16, 64, 256, 8), (3, 8, 16, 128, 512, 8), (40, 4, 8, 64, 192, 16),
+                                          (96, 8, 32, 64, 128, 32)])
+def test_moe_w2_gemv(C, T, k, E, N, K, MB):
+    g = torch.Generator().manual_seed(T * 31 + E)
+    codes, sc, pool = _expert_pool(E, N, K, g)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).int()
+    R = T * k
+    P = R // MB + min(E, R)
+    dev = lambda t: t.to(DEV)  # noqa: E731
+    rank, stok, posof = (torch.empty(R, dtype=torch.int32, device=DEV) for _ in range(3))
+    pairs = torch.empty(P, 4, dtype=torch.int32, device=DEV); npairs = torch.zeros(1, dtype=torch.int32, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    C.build_pairs(dev(ids), E, MB, rank, stok, posof, pairs, npairs, status)
+    assert int(status) == 0
+    x = torch.randn(T, K, generator=g)
+    q, s = fp8.quant_act_fp8(x)
+    qw2 = fp8.to_w2_layout(q.view(torch.uint8))
+    out = torch.full((R, N), float("nan"), device=DEV)
+    slot_table = torch.arange(E, dtype=torch.int32, device=DEV)
+    miss = torch.zeros(1, dtype=torch.int32, device=DEV)
+    C.moe_w2_gemv(dev(qw2), dev(s), stok, pairs, npairs, dev(pool), 0, N * K // 4, slot_table, out, N, K, MB, miss)
+    A = fp8.dequant_act_fp8(q, s).double()
+    posof_c = posof.cpu().long()
+    for t in range(T):
+        for j in range(k):
+            e = int(ids[t, j])
+            W = codebook.dequant_codes(codes[e], sc[e]).double()
+            ref = A[t] @ W.t()
+            assert rel(out[posof_c[t * k + j]].cpu(), ref) < 1e-4, (t, j)
+    assert int(miss) == 0
+    # a missing expert writes zeros and counts a miss
+    slot_table[int(ids[0, 0])] = -1
+    C.moe_w2_gemv(dev(qw2), dev(s), stok, pairs, npairs, dev(pool), 0, N * K // 4, slot_table, out, N, K, MB, miss)
+    assert int(miss) >= 1
+    assert (out[posof_c[0]] == 0).all()
+
+
+def test_moe_w2_scale_folding_wide_exponent_range(C):
+    """Neighbouring k32 blocks whose exponents differ by up to 9 stay exact."""
+    g = torch.Generator().manual_seed(5)
+    E, N, K, T = 2, 32, 256, 2
+    codes, sc, pool = _expert_pool(E, N, K, g, lo=110, hi=119)
+    ids = torch.tensor([[0, 1], [1, 0]], dtype=torch.int32)
+    R, MB = 4, 8
+    rank, stok, posof = (torch.empty(R, dtype=torch.int32, device=DEV) for _ in range(3))
+    pairs = torch.empty(R // MB + 2, 4, dtype=torch.int32, device=DEV); npairs = torch.zeros(1, dtype=torch.int32, device=DEV)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    C.build_pairs(ids.to(DEV), E, MB, rank, stok, posof, pairs, npairs, st)
+    x = torch.randn(T, K, generator=g)
+    q, s = fp8.quant_act_fp8(x)
+    out = torch.empty(R, N, device=DEV)
+    C.moe_w2_gemv(fp8.to_w2_layout(q.view(torch.uint8)).to(DEV), s.to(DEV), stok, pairs, npairs, pool.to(DEV), 0,
+                  N * K // 4, torch.arange(E, dtype=torch.int32, device=DEV), out, N, K, MB, None)
+    A = fp8.dequant_act_fp8(q, s).double()
+    for t in range(T):
+        for j in range(2):
+            W = codebook.dequant_codes(codes[int(ids[t, j])], sc[int(ids[t, j])]).double()
+            assert rel(out[int(posof[t * 2 + j])].cpu(), A[t] @ W.t()) < 1e-4
+
+
+def test_moe_combine(C):
+    g = torch.Generator().manual_seed(3)
+    T, k, H = 5, 4, 256
+    y = torch.randn(T * k, H, generator=g)
+    posof = torch.randperm(T * k, generator=g).int()
+    w = torch.rand(T, k, generator=g)
+    res = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    sh = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=DEV)
+    C.moe_combine(y.to(DEV), posof.to(DEV), w.to(DEV), res.to(DEV), sh.to(DEV), out, None)
+    ref = res.float() + sh.float() + sum(w[:, j:j + 1] * y[posof.view(T, k)[:, j].long()] for j in range(k))
+    assert rel(out.cpu().float(), ref) < 1e-2
+
+
+# ------------------------------------------------------------------------- attention
+def _paged_cache(n_blocks, g):
+    kv = torch.zeros(n_blocks, 64, 584, dtype=torch.bfloat16)
+    kv[:, :, :576] = (torch.randn(n_blocks, 64, 576, generator=g)).to(torch.bfloat16)
+    return kv
+
+
+@pytest.mark.parametrize("Hh,ctx,nsplit", [(32, [1, 65, 300], 4), (16, [130], 1), (8, [64, 7], 8)])
+def test_mla_decode(C, Hh, ctx, nsplit):
+    g = torch.Generator().manual_seed(Hh + len(ctx))
+    nseq = len(ctx)
+    maxb = max(-(-c // 64) for c in ctx)
+    nblk = nseq * maxb + 3
+    kv = _paged_cache(nblk, g)
+    perm = torch.randperm(nblk - 1, generator=g)[: nseq * maxb] + 1
+    bt = perm.view(nseq, maxb).int()
+    q = (torch.randn(nseq, Hh, 576, generator=g) * 0.3).to(torch.bfloat16)
+    seq = torch.arange(nseq, dtype=torch.int32)
+    pos = torch.tensor([c - 1 for c in ctx], dtype=torch.int32)
+    opart = torch.empty(nsplit, nseq, Hh, 512, device=DEV)
+    ml = torch.empty(nsplit, nseq, Hh, 2, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    scale = 1 / math.sqrt(192)
+    C.mla_decode(q.to(DEV), kv.to(DEV), bt.to(DEV), seq.to(DEV), pos.to(DEV), opart, ml, scale, status)
+    out = torch.empty(nseq, Hh, 512, dtype=torch.bfloat16, device=DEV)
+    oq = torch.empty(nseq, Hh, 512, dtype=torch.uint8, device=DEV); os_ = torch.empty(nseq, Hh, 8, dtype=torch.uint8, device=DEV)
+    C.mla_combine(opart, ml, out, oq, os_)
+    assert int(status) == 0
+    for i, c in enumerate(ctx):
+        rows = torch.cat([kv[bt[i, p // 64], p % 64:p % 64 + 1] for p in range(c)])[:, :576].float()
+        s = (q[i].float() @ rows.t()) * scale
+        ref = torch.softmax(s, -1) @ rows[:, :512]
+        assert rel(out[i].cpu().float(), ref) < 2e-2, i
+        deq = fp8.dequant_act_fp8(oq[i].cpu().view(torch.float8_e4m3fn).reshape(Hh, 512), os_[i].cpu())
+        assert rel(deq, ref) < 5e-2
+
+
+@pytest.mark.parametrize("lens,Hh", [([200], 2), ([130, 70, 1], 3)])
+def test_mla_prefill(C, lens, Hh):
+    g = torch.Generator().manual_seed(sum(lens))
+    T = sum(lens)
+    q = (torch.randn(T, Hh, 192, generator=g) * 0.5).to(torch.bfloat16)
+    kvb = (torch.randn(T, Hh, 256, generator=g) * 0.5).to(torch.bfloat16)
+    kr = (torch.randn(T, 64, generator=g) * 0.5).to(torch.bfloat16)
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32)
+    out = torch.empty(T, Hh * 128, dtype=torch.bfloat16, device=DEV)
+    oq = torch.empty(T, Hh * 128, dtype=torch.uint8, device=DEV); os_ = torch.empty(T, Hh * 2, dtype=torch.uint8, device=DEV)
+    scale = 1 / math.sqrt(192)
+    C.mla_prefill(q.to(DEV), kvb.to(DEV), kr.to(DEV), cu.to(DEV), max(lens), scale, oq, os_, out)
+    for si, n in enumerate(lens):
+        s0 = int(cu[si])
+        for h in range(Hh):
+            qq = q[s0:s0 + n, h].float()
+            kk = torch.cat([kvb[s0:s0 + n, h, :128].float(), kr[s0:s0 + n].float()], -1)
+            vv = kvb[s0:s0 + n, h, 128:].float()
+            s = (qq @ kk.t()) * scale
+            s = s.masked_fill(torch.ones(n, n).triu(1).bool(), float("-inf"))
+            ref = torch.softmax(s, -1) @ vv
+            assert rel(out[s0:s0 + n, h * 128:(h + 1) * 128].cpu().float(), ref) < 2e-2, (si, h)
+    deq = fp8.dequant_act_fp8(oq.cpu().view(torch.float8_e4m3fn), os_.cpu())
+    assert rel(deq, out.cpu().float()) < 5e-2
+
+
+def test_kv_prep_bf16_and_nvfp4(C):
+    g = torch.Generator().manual_seed(11)
+    T = 5
+    kva = (torch.randn(T, 576 + 16, generator=g)).to(torch.bfloat16)[:, :576]
+    w = (torch.rand(512, generator=g) + 0.5).to(torch.bfloat16)
+    from vllm_moet_b200.config import ds4_flash_config
+    from vllm_moet_b200.models.reference import rope_cos_sin, apply_rope
+    cs = rope_cos_sin(ds4_flash_config(), 64)
+    pos = torch.tensor([0, 3, 9, 17, 40], dtype=torch.int32)
+    slots = torch.tensor([5, -1, 64, 70, 127], dtype=torch.int64)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    cache = torch.zeros(2, 64, 584, dtype=torch.bfloat16, device=DEV)
+    lat = torch.empty(T, 512, dtype=torch.bfloat16, device=DEV); rp = torch.empty(T, 64, dtype=torch.bfloat16, device=DEV)
+    C.kv_prep(kva.to(DEV), 512, 64, w.to(DEV), 1e-6, pos.to(DEV), cs.to(DEV), slots.to(DEV), 1, cache, lat, rp,
+              None, None, st)
+    assert int(st) == 0
+    x = kva[:, :512].float()
+    ref_lat = (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float())
+    assert rel(lat.cpu().float(), ref_lat) < 1e-2
+    ref_rope = apply_rope(kva[:, 512:].float(), cs[pos.long()])
+    assert rel(rp.cpu().float(), ref_rope) < 1e-2
+    flat = cache.view(-1, 584).cpu()
+    for t in range(T):
+        if slots[t] >= 0:
+            assert torch.equal(flat[slots[t], :512], lat[t].cpu())
+            assert torch.equal(flat[slots[t], 512:576], rp[t].cpu())
+    # NVFP4 rows are byte-identical to the golden encoder applied to the same latent/rope
+    c4 = torch.zeros(128, 352, dtype=torch.uint8, device=DEV)
+    C.kv_prep(kva.to(DEV), 512, 64, w.to(DEV), 1e-6, pos.to(DEV), cs.to(DEV), slots.to(DEV), 2, c4, lat, rp,
+              None, None, st)
+    enc = kv_nvfp4.encode(lat.cpu().float(), rp.cpu().float())
+    for t in range(T):
+        if slots[t] >= 0:
+            assert torch.equal(c4[slots[t]].cpu(), enc[t]), t
+    # out-of-range slot -> status, no trap
+    bad = torch.tensor([1000, 0, 1, 2, 3], dtype=torch.int64, device=DEV)
+    C.kv_prep(kva.to(DEV), 512, 64, w.to(DEV), 1e-6, pos.to(DEV), cs.to(DEV), bad, 2, c4, None, None, None, None, st)
+    torch.cuda.synchronize()
+    assert int(st) == 1
+
+
+# ------------------------------------------------------------------------- load-time quantiser + sampling
+def test_w2_quant_pack_matches_golden(C):
+    g = torch.Generator().manual_seed(2)
+    N, K = 48, 192
+    w = torch.randn(N, K, generator=g) * 0.02
+    ts = float(w.abs().max()) / (6 * 448)
+    packed = torch.empty(N, K // 2, dtype=torch.uint8, device=DEV)
+    sf = torch.empty(N, K // 16, dtype=torch.uint8, device=DEV)
+    C.nvfp4_quant(w.to(DEV), ts, packed, sf)
+    rp, rsf, rts = codebook.f32_to_nvfp4(w, ts)
+    assert torch.equal(packed.cpu(), rp)
+    assert torch.equal(sf.cpu(), rsf.view(torch.uint8))
+    cp = torch.empty(N * K // 4, dtype=torch.uint8, device=DEV)
+    sp = torch.empty(N * K // 32, dtype=torch.uint8, device=DEV)
+    fp = torch.empty(N * K // 2, dtype=torch.uint8, device=DEV)
+    cnt = torch.zeros(2, dtype=torch.int64, device=DEV)
+    C.w2_quant_pack(packed, sf, ts, 0, cp, sp, fp, cnt)
+    codes, sc, nib = codebook.nvfp4_to_codes_scales(rp, rsf, rts, mode="sign", want_nibbles=True)
+    assert torch.equal(cp.cpu(), planes.pack_codes(codes))
+    assert torch.equal(sp.cpu(), planes.pack_scales(sc))
+    assert torch.equal(fp.cpu(), planes.pack_fp4(nib))
+
+
+def test_argmax_lse(C):
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(6, 129280, generator=g)
+    x[2, 77] = 50.0
+    ids = torch.empty(6, dtype=torch.int32, device=DEV); lse = torch.empty(6, device=DEV)
+    C.argmax_lse(x.to(DEV), ids, lse, None)
+    assert torch.equal(ids.cpu().long(), x.argmax(-1))
+    assert rel(lse.cpu(), torch.logsumexp(x, -1)) < 1e-5
+
+
+def test_mtp_accept_and_finalize(C):
+    tgt = torch.tensor([[5, 6, 7], [5, 6, 7], [5, 6, 7]], dtype=torch.int32)
+    tok = torch.tensor([[1, 5, 6], [1, 5, 9], [1, 4, 6]], dtype=torch.int32)
+    out = torch.empty(3, 3, dtype=torch.int32, device=DEV); acc = torch.empty(3, dtype=torch.int32, device=DEV)
+    C.mtp_accept(tgt.to(DEV), tok.to(DEV), out, acc, None)
+    assert acc.cpu().tolist() == [2, 1, 0]
+    assert out.cpu().tolist() == [[5, 6, 7], [5, 6, -1], [5, -1, -1]]
+    drafts = torch.tensor([[8, 9], [8, 9], [8, 9]], dtype=torch.int32, device=DEV)
+    toks = tok.to(DEV).clone(); pos = torch.tensor([10, 10, 10], dtype=torch.int32, device=DEV)
+    C.mtp_finalize(tgt.to(DEV), acc, drafts, toks, pos, None)
+    assert toks.cpu().tolist() == [[7, 8, 9], [6, 8, 9], [5, 8, 9]]
+    assert pos.cpu().tolist() == [13, 12, 11]
