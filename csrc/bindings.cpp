@@ -54,7 +54,7 @@ void w2_quant_pack(torch::Tensor packed, torch::Tensor sf, double ts, int64_t ze
                    c10::optional<torch::Tensor> counters);
 // sampling.cu
 void argmax_lse(torch::Tensor logits, torch::Tensor ids, c10::optional<torch::Tensor> lse,
-                c10::optional<torch::Tensor> maxv);
+                c10::optional<torch::Tensor> maxv, c10::optional<torch::Tensor> status);
 void mtp_accept(torch::Tensor targets, torch::Tensor tokens, torch::Tensor out_tokens, torch::Tensor n_acc,
                 c10::optional<torch::Tensor> active);
 void mtp_finalize(torch::Tensor targets, torch::Tensor n_acc, torch::Tensor drafts, torch::Tensor tokens,

@@ -16,6 +16,7 @@ enum Status : int {
   kBadIndex = 1,      // an index (slot, expert, position) was out of range
   kTimeout = 2,       // a bounded wait gave up
   kBadSize = 3,
+  kBadValue = 4,     // a non-finite value where a finite one is required
 };
 
 MOET_DEVICE void set_status(int* status, int code) {

@@ -106,10 +106,10 @@ __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x_in,
   }
   if (y_out) {
 #pragma unroll
-    for (int i = 0; i < VEC; i++) y_out[(size_t)row * H + k0 + i] = __float2bfloat16(v[i]);
+    for (int i = 0; i < VEC; i++) y_out[(size_t)row * ostride + k0 + i] = __float2bfloat16(v[i]);
   }
-  if (q0) quant_store<VEC>(v, row, k0, H, 0, q0, s0);
-  if (q1) quant_store<VEC>(v, row, k0, H, 1, q1, s1);
+  if (q0) quant_store<VEC>(v, row, k0, H, 0, q0, s0, ostride);
+  if (q1) quant_store<VEC>(v, row, k0, H, 1, q1, s1, ostride);
 }
 
 // SwiGLU: in [rows, 2I] f32 (gate | up), out e4m3 [rows, I].
@@ -165,12 +165,12 @@ void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> add, c10::optio
   TORCH_CHECK(H % 64 == 0, "H must be a multiple of 64");
   if (rows == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  int vec = 16;
-  while (H / vec > 1024) vec *= 2;
-  TORCH_CHECK(vec == 16, "H too large for rmsnorm_quant (max 16384)");
-  int threads = H / 16;
-  TORCH_CHECK(threads % 4 == 0 && threads >= 32, "H must be >= 512");
-  rmsnorm_quant_kernel<16><<<rows, threads, 0, stream>>>(
+  TORCH_CHECK(H <= 16384, "H too large for rmsnorm_quant (max 16384)");
+  const int vec = H >= 512 ? 16 : (H >= 256 ? 8 : 4);
+  TORCH_CHECK(H >= 128, "rmsnorm_quant: H must be >= 128");
+  const int threads = H / vec;
+  auto kern = vec == 16 ? rmsnorm_quant_kernel<16> : (vec == 8 ? rmsnorm_quant_kernel<8> : rmsnorm_quant_kernel<4>);
+  kern<<<rows, threads, 0, stream>>>(
       (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)opt_ptr(add),
       (__nv_bfloat16*)opt_ptr(x_out), (const __nv_bfloat16*)w.data_ptr(), (float)eps, H,
       (__nv_bfloat16*)opt_ptr(y_out), (uint8_t*)opt_ptr(q0), (uint8_t*)opt_ptr(s0),

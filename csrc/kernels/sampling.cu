@@ -14,7 +14,8 @@ namespace moet {
 
 template <typename T>
 __global__ void argmax_lse_kernel(const T* __restrict__ logits, long long stride, int V,
-                                  int* __restrict__ ids, float* __restrict__ lse, float* __restrict__ maxv) {
+                                  int* __restrict__ ids, float* __restrict__ lse, float* __restrict__ maxv,
+                                  int* __restrict__ status) {
   const int row = blockIdx.x;
   const T* x = logits + (size_t)row * stride;
   float bv = -INFINITY; int bi = 0x7fffffff;
@@ -54,7 +55,12 @@ __global__ void argmax_lse_kernel(const T* __restrict__ logits, long long stride
       lse[row] = m + __logf(tot);
     }
   }
-  if (threadIdx.x == 0) { ids[row] = si[0]; if (maxv) maxv[row] = m; }
+  if (threadIdx.x == 0) {
+    int id = si[0];
+    if (id < 0 || id >= V) { id = 0; set_status(status, kBadValue); }  // no finite logit
+    ids[row] = id;
+    if (maxv) maxv[row] = m;
+  }
 }
 
 // targets [B, 1+k] (argmax of the verify rows), tokens [B, 1+k] (this step's inputs;
@@ -90,17 +96,18 @@ __global__ void mtp_finalize_kernel(const int* __restrict__ targets, const int* 
 using namespace moet;
 
 void argmax_lse(torch::Tensor logits, torch::Tensor ids, c10::optional<torch::Tensor> lse,
-                c10::optional<torch::Tensor> maxv) {
+                c10::optional<torch::Tensor> maxv, c10::optional<torch::Tensor> status) {
   const int R = logits.size(0), V = logits.size(1);
   TORCH_CHECK(logits.stride(1) == 1, "argmax_lse: inner stride 1");
   if (R == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   if (logits.scalar_type() == at::kFloat)
     argmax_lse_kernel<float><<<R, 1024, 0, stream>>>(logits.data_ptr<float>(), logits.stride(0), V, ids.data_ptr<int>(),
-                                                     (float*)opt_ptr(lse), (float*)opt_ptr(maxv));
+                                                     (float*)opt_ptr(lse), (float*)opt_ptr(maxv), (int*)opt_ptr(status));
   else
     argmax_lse_kernel<__nv_bfloat16><<<R, 1024, 0, stream>>>((const __nv_bfloat16*)logits.data_ptr(), logits.stride(0), V,
-                                                             ids.data_ptr<int>(), (float*)opt_ptr(lse), (float*)opt_ptr(maxv));
+                                                             ids.data_ptr<int>(), (float*)opt_ptr(lse), (float*)opt_ptr(maxv),
+                                                             (int*)opt_ptr(status));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

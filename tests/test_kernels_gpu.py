@@ -339,7 +339,7 @@ def test_argmax_lse(C):
     x = torch.randn(6, 129280, generator=g)
     x[2, 77] = 50.0
     ids = torch.empty(6, dtype=torch.int32, device=DEV); lse = torch.empty(6, device=DEV)
-    C.argmax_lse(x.to(DEV), ids, lse, None)
+    C.argmax_lse(x.to(DEV), ids, lse, None, None)
     assert torch.equal(ids.cpu().long(), x.argmax(-1))
     assert rel(lse.cpu(), torch.logsumexp(x, -1)) < 1e-5
 
@@ -356,3 +356,20 @@ def test_mtp_accept_and_finalize(C):
     C.mtp_finalize(tgt.to(DEV), acc, drafts, toks, pos, None)
     assert toks.cpu().tolist() == [[7, 8, 9], [6, 8, 9], [5, 8, 9]]
     assert pos.cpu().tolist() == [13, 12, 11]
+
+
+def test_rmsnorm_quant_output_stride(C):
+    """Two norms writing the halves of one [T, 2H] FP8 operand (MTP concat)."""
+    T, H = 6, 1024
+    a = (torch.randn(T, H) * 0.02).to(torch.bfloat16).to(DEV)
+    b = torch.randn(T, H).to(torch.bfloat16).to(DEV)
+    w = torch.ones(H, dtype=torch.bfloat16, device=DEV)
+    q = torch.zeros(T, 2 * H, dtype=torch.uint8, device=DEV)
+    s = torch.full((T, 2 * H // 64), 255, dtype=torch.uint8, device=DEV)
+    C.rmsnorm_quant(a, None, None, w, 1e-6, None, q, s, None, None, 2 * H)
+    C.rmsnorm_quant(b, None, None, w, 1e-6, None, q[:, H:], s[:, H // 64:], None, None, 2 * H)
+    qa = torch.empty(T, H, dtype=torch.uint8, device=DEV); sa = torch.empty(T, H // 64, dtype=torch.uint8, device=DEV)
+    C.rmsnorm_quant(a, None, None, w, 1e-6, None, qa, sa, None, None, 0)
+    assert torch.equal(q[:, :H], qa) and torch.equal(s[:, :H // 64], sa)
+    C.rmsnorm_quant(b, None, None, w, 1e-6, None, qa, sa, None, None, 0)
+    assert torch.equal(q[:, H:], qa) and torch.equal(s[:, H // 64:], sa)

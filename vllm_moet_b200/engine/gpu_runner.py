@@ -87,13 +87,15 @@ class NativeRunner:
         self.cos_sin = rope_cos_sin(cfg, ecfg.max_model_len + 64, self.dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.miss = torch.zeros(1, dtype=torch.int32, device=self.dev)
-        self.ws_decode = Workspace(self.dev)
+        self.ws_decode_by_bucket = {}
         self.ws_prefill = Workspace(self.dev)
-        self.ws = self.ws_decode
+        self.ws = self.ws_prefill
         self.scale = 1.0 / math.sqrt(cfg.qk_head_dim)
         self.graphs = {}
         self.tp_group = None
         self.nsplit = 8
+        import os
+        self.debug_finite = os.environ.get("MOET_DEBUG_FINITE", "0") == "1"
 
     # ------------------------------------------------------------------ helpers
     def _fp8(self, name, T, K):
@@ -227,12 +229,22 @@ class NativeRunner:
             self._tp_allreduce(part)
             torch.add(x, part, out=out)
 
+    def _check(self, name, t):
+        """Debug aid (MOET_DEBUG_FINITE=1, eager only): raise at the first non-finite stage output."""
+        if self.debug_finite and not torch.cuda.is_current_stream_capturing():
+            bad = ~torch.isfinite(t.float())
+            if bool(bad.any()):
+                rows = bad.view(t.shape[0], -1).any(-1).nonzero().flatten()[:8].tolist()
+                raise FloatingPointError(f"non-finite values after {name}: shape {tuple(t.shape)}, rows {rows}")
+
     def _layer(self, lw, x, ctx, cache, li):
         H = self.cfg.hidden
         x2 = self.ws.get("x_mid", (ctx.T, H), torch.bfloat16)
         self._attention(lw, x, ctx, cache, li, x2)
+        self._check(f"attention[{li}] ({ctx.mode})", x2)
         x3 = self.ws.get("x_a" if li % 2 == 0 else "x_b", (ctx.T, H), torch.bfloat16)
         self._ffn(lw, x2, ctx, x3)
+        self._check(f"ffn[{li}] ({ctx.mode})", x3)
         return x3
 
     # ------------------------------------------------------------------ model pieces
@@ -255,6 +267,7 @@ class NativeRunner:
                         cfg.rms_eps, hid, fq, fs, None, None, 0)
         logits = self.ws.get(tag + ".logits", (T, cfg.vocab), torch.float32)
         self._gemv(fq, fs, self.mw.lm_head, logits)
+        self._check(f"lm_head ({tag})", logits)
         return hid, logits
 
     def _mtp(self, hidden, next_tokens, ctx: StepCtx):
@@ -269,6 +282,7 @@ class NativeRunner:
                         2 * H)
         xm = self.ws.get("xm", (T, H), torch.bfloat16)
         self._gemv(ehq, ehs, m.eh_proj, xm)
+        self._check("mtp eh_proj", xm)
         x = self._layer(m.layer, xm, ctx, self.kv[-1], 0)
         return self._final(x, None, "mtp")
 
@@ -280,9 +294,18 @@ class NativeRunner:
         first generated token of each prompt."""
         self.ws = self.ws_prefill
         try:
-            return self._prefill(prompts, block_tables, seq_rows, state)
+            out = self._prefill(prompts, block_tables, seq_rows, state)
         finally:
-            self.ws = self.ws_decode
+            self.ws = self.ws_prefill
+        self.check_status("prefill")
+        return out
+
+    def check_status(self, where: str):
+        code = int(self.status.item())
+        if code != 0:
+            self.status.zero_()
+            names = {1: "index out of range", 2: "bounded wait timed out", 3: "bad size", 4: "non-finite logits"}
+            raise RuntimeError(f"device status {code} ({names.get(code, '?')}) during {where}")
 
     def _prefill(self, prompts, block_tables, seq_rows, state):
         dev, C = self.dev, self.C
@@ -301,7 +324,7 @@ class NativeRunner:
         xl = x[last].contiguous()
         hid_last, logits = self._final(xl, None, "main")
         tgt = self.ws.get("pf.tgt", (len(prompts),), torch.int32)
-        C.argmax_lse(logits, tgt, None, None)
+        C.argmax_lse(logits, tgt, None, None, self.status)
         B = len(prompts)
         if self.k == 0:
             state.set_rows(seq_rows, tgt, torch.tensor(lens, dtype=torch.int32, device=dev), None)
@@ -318,7 +341,7 @@ class NativeRunner:
         # only the last row of each prompt matters; argmax over those rows
         ml = mlog[last].contiguous()
         d1 = self.ws.get("pf.d1", (B,), torch.int32)
-        C.argmax_lse(ml, d1, None, None)
+        C.argmax_lse(ml, d1, None, None, self.status)
         drafts[:, 0] = d1
         h_prev = mh[last].contiguous()
         cur_pos = torch.tensor(lens, dtype=torch.int32, device=dev)  # position of the first generated token
@@ -330,15 +353,31 @@ class NativeRunner:
             ctx2 = StepCtx(T=B, pos=p2, seq=s2, slot=slot2, block_table=bt, mode="decode", mb=8)
             h_prev, lg = self._mtp(h_prev.clone(), prev_tok, ctx2)
             dj = self.ws.get("pf.dj", (B,), torch.int32)
-            C.argmax_lse(lg, dj, None, None)
+            C.argmax_lse(lg, dj, None, None, self.status)
             drafts[:, j] = dj
             prev_tok = dj.clone()
         state.set_rows(seq_rows, tgt, cur_pos, drafts)
         return tgt
 
     # ------------------------------------------------------------------ decode
+    def _bucket_ws(self, B):
+        ws = self.ws_decode_by_bucket.get(B)
+        if ws is None:
+            ws = self.ws_decode_by_bucket[B] = Workspace(self.dev)
+        return ws
+
     def decode_body(self, st):
-        """One MTP decode step over the device state `st` (all tensors static)."""
+        """One MTP decode step over the device state `st` (all tensors static).
+        Each batch bucket owns its workspace: a captured graph keeps the
+        addresses it was recorded with."""
+        prev = self.ws
+        self.ws = self._bucket_ws(st.B)
+        try:
+            self._decode_body(st)
+        finally:
+            self.ws = prev
+
+    def _decode_body(self, st):
         C, k = self.C, self.k
         B = st.B
         kp1 = k + 1
@@ -351,7 +390,7 @@ class NativeRunner:
                       mb=8 if T * self.cfg.top_k <= 256 else 16)
         x = self._main(st.tokens.view(-1), ctx)
         hid, logits = self._final(x, None, "main")
-        C.argmax_lse(logits, st.targets.view(-1), None, None)
+        C.argmax_lse(logits, st.targets.view(-1), None, None, self.status)
         C.mtp_accept(st.targets, st.tokens, st.out_tokens, st.n_acc, st.active)
         if k == 0:
             st.seq_pos.add_(st.active)
@@ -360,7 +399,7 @@ class NativeRunner:
         # MTP pass 1 over the verify rows: (h_j, target_j) at position p + j
         mh, mlog = self._mtp(hid, st.targets.view(-1), ctx)
         am = self.ws.get("dec.am", (T,), torch.int32)
-        C.argmax_lse(mlog, am, None, None)
+        C.argmax_lse(mlog, am, None, None, self.status)
         sel = (st.arange_b * kp1 + st.n_acc).long()
         prev_tok = am[sel]
         st.drafts[:, 0] = prev_tok
@@ -374,7 +413,7 @@ class NativeRunner:
                            mode="decode", mb=8)
             h_prev, lg = self._mtp(h_prev, prev_tok, ctx2)
             dj = self.ws.get("dec.dj", (B,), torch.int32)
-            C.argmax_lse(lg, dj, None, None)
+            C.argmax_lse(lg, dj, None, None, self.status)
             st.drafts[:, j] = dj
             prev_tok = dj
         C.mtp_finalize(st.targets, st.n_acc, st.drafts, st.tokens, st.seq_pos, st.active)
@@ -390,7 +429,7 @@ class NativeRunner:
                 self.decode_body(st)
         torch.cuda.current_stream().wait_stream(s)
         self.graphs[st.B] = g
-        self.ws_decode.frozen = True
+        self._bucket_ws(st.B).frozen = True
         return g
 
     def decode_body_eager_warm(self, st):

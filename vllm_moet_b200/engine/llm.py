@@ -228,8 +228,7 @@ class LLM:
             pin_acc.copy_(st.n_acc, non_blocking=True)
             torch.cuda.current_stream().synchronize()
             t_decode += time.perf_counter() - t0
-            if int(runner.status.item()) != 0:
-                raise RuntimeError(f"device kernel reported status {int(runner.status.item())}")
+            runner.check_status("decode step")
             steps += 1
             for i, r in enumerate(rows):
                 if r is None:
