@@ -216,3 +216,50 @@ void build_pairs(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor ra
                                              n_pairs.data_ptr<int>(), status.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
+
+// ---------------------------------------------------------------------------
+// Scratch-free C entry point (declared in moe_route_noalloc.h): the same
+// pair-list kernel, with its per-routing rank scratch in a static device array
+// instead of a caller-provided buffer.
+#include <mutex>
+#include "moe_route_noalloc.h"
+
+namespace moet_noalloc {
+static __device__ __align__(256) int g_rank_scratch[MOET_NOALLOC_MAX_ROUTINGS];
+constexpr int kMaxDevices = 128;
+static int* g_scratch_addr[kMaxDevices];  // device address of g_rank_scratch, per device
+static std::mutex g_mu;
+}  // namespace moet_noalloc
+
+extern "C" int moet_build_pairs_noalloc(const int* topk_ids, int num_tokens, int top_k, int num_experts,
+                                        int rows_per_pair, int* sorted_tok, int* pos_of, int* pairs,
+                                        int max_pairs, int* n_pairs, int* status, cudaStream_t stream) {
+  using namespace moet_noalloc;
+  if (!topk_ids || !sorted_tok || !pos_of || !pairs || !n_pairs || !status) return MOET_NOALLOC_EINVAL;
+  if (num_tokens < 0 || top_k < 1 || top_k > 32 || num_experts < 1 || num_experts > moet::kMaxE ||
+      rows_per_pair < 1)
+    return MOET_NOALLOC_EINVAL;
+  const long long R = (long long)num_tokens * top_k;
+  if (R > MOET_NOALLOC_MAX_ROUTINGS) return MOET_NOALLOC_ETOOBIG;
+  if ((long long)max_pairs < R / rows_per_pair + std::min<long long>(num_experts, R)) return MOET_NOALLOC_EINVAL;
+  int dev = 0;
+  cudaError_t rc = cudaGetDevice(&dev);
+  if (rc != cudaSuccess) return (int)rc;
+  if (dev < 0 || dev >= kMaxDevices) return MOET_NOALLOC_EINVAL;
+  int* scratch;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!g_scratch_addr[dev]) {
+      void* p = nullptr;
+      rc = cudaGetSymbolAddress(&p, g_rank_scratch);
+      if (rc != cudaSuccess) return (int)rc;
+      g_scratch_addr[dev] = static_cast<int*>(p);
+    }
+    scratch = g_scratch_addr[dev];
+  }
+  moet::build_pairs_kernel<<<1, 1024, 0, stream>>>(topk_ids, (int)R, top_k, num_experts, rows_per_pair, scratch,
+                                                  sorted_tok, pos_of, reinterpret_cast<int4*>(pairs), n_pairs,
+                                                  status);
+  rc = cudaGetLastError();
+  return rc == cudaSuccess ? MOET_NOALLOC_OK : (int)rc;
+}
