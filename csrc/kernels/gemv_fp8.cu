@@ -55,28 +55,41 @@ __global__ void __launch_bounds__(256) gemv_fp8_kernel(GemvArgs p) {
   const uint8_t* xbase = A + 16 * t;
   const int tg = tok0 + g, tc = tok0 + 2 * t;
 
-#pragma unroll 2
-  for (int c = warp; c < nchunks; c += nwarps) {
-    const uint4 wa = ldg_stream_u4(wa_p + (size_t)c * 64);
-    const uint4 wb = ldg_stream_u4(wb_p + (size_t)c * 64);
-    const float ws = ue8m0_to_float(sw_row[c >> 1]);
-    const uint32_t a0[4] = {wa.x, wb.x, wa.y, wb.y};
-    const uint32_t a1[4] = {wa.z, wb.z, wa.w, wb.w};
+  // Each warp takes U consecutive chunks per step and issues all of their weight
+  // loads before consuming any, keeping U * 1 KiB per warp in flight.
+  constexpr int U = NT <= 1 ? 8 : (NT <= 2 ? 4 : 2);
+  for (int cb = warp * U; cb < nchunks; cb += nwarps * U) {
+    uint4 wa[U], wb[U];
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-      uint4 x = make_uint4(0, 0, 0, 0);
-      const int tok = tg + nt * 8;
-      if (tok < p.T) x = __ldg(reinterpret_cast<const uint4*>(xbase + (size_t)tok * p.a_row_stride + (size_t)c * 64));
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      mma_e4m3_16832(d, a0, x.x, x.y, d);
-      mma_e4m3_16832(d, a1, x.z, x.w, d);
-      const int c0 = tc + nt * 8;
-      const float s0 = c0 < p.T ? ws * ue8m0_to_float(sA[(size_t)c0 * p.sa_row_stride + c]) : 0.f;
-      const float s1 = c0 + 1 < p.T ? ws * ue8m0_to_float(sA[(size_t)(c0 + 1) * p.sa_row_stride + c]) : 0.f;
-      acc[nt][0] = fmaf(d[0], s0, acc[nt][0]);
-      acc[nt][1] = fmaf(d[1], s1, acc[nt][1]);
-      acc[nt][2] = fmaf(d[2], s0, acc[nt][2]);
-      acc[nt][3] = fmaf(d[3], s1, acc[nt][3]);
+    for (int u = 0; u < U; u++) {
+      if (cb + u < nchunks) {
+        wa[u] = ldg_stream_u4(wa_p + (size_t)(cb + u) * 64);
+        wb[u] = ldg_stream_u4(wb_p + (size_t)(cb + u) * 64);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int c = cb + u;
+      if (c >= nchunks) break;
+      const float ws = ue8m0_to_float(sw_row[c >> 1]);
+      const uint32_t a0[4] = {wa[u].x, wb[u].x, wa[u].y, wb[u].y};
+      const uint32_t a1[4] = {wa[u].z, wb[u].z, wa[u].w, wb[u].w};
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {
+        uint4 x = make_uint4(0, 0, 0, 0);
+        const int tok = tg + nt * 8;
+        if (tok < p.T) x = __ldg(reinterpret_cast<const uint4*>(xbase + (size_t)tok * p.a_row_stride + (size_t)c * 64));
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_e4m3_16832(d, a0, x.x, x.y, d);
+        mma_e4m3_16832(d, a1, x.z, x.w, d);
+        const int c0 = tc + nt * 8;
+        const float s0 = c0 < p.T ? ws * ue8m0_to_float(sA[(size_t)c0 * p.sa_row_stride + c]) : 0.f;
+        const float s1 = c0 + 1 < p.T ? ws * ue8m0_to_float(sA[(size_t)(c0 + 1) * p.sa_row_stride + c]) : 0.f;
+        acc[nt][0] = fmaf(d[0], s0, acc[nt][0]);
+        acc[nt][1] = fmaf(d[1], s1, acc[nt][1]);
+        acc[nt][2] = fmaf(d[2], s0, acc[nt][2]);
+        acc[nt][3] = fmaf(d[3], s1, acc[nt][3]);
+      }
     }
   }
 
@@ -151,14 +164,16 @@ void gemv_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tensor 
   p.out_f32 = out.scalar_type() == at::kFloat;
   TORCH_CHECK(p.out_f32 || out.scalar_type() == at::kBFloat16, "gemv_fp8: out must be bf16 or f32");
   const int nchunks = K / 64;
-  const int nwarps = std::max(1, std::min(8, nchunks));
   auto stream = at::cuda::getCurrentCUDAStream();
   auto launch = [&](auto nt_const) {
     constexpr int NT = decltype(nt_const)::value;
+    constexpr int U = NT <= 1 ? 8 : (NT <= 2 ? 4 : 2);
+    const int nwarps = std::max(1, std::min(8, (nchunks + U - 1) / U));
     dim3 grid((N + 15) / 16, (T + 8 * NT - 1) / (8 * NT), B);
     size_t smem = nwarps > 1 ? (size_t)nwarps * NT * 4 * 32 * sizeof(float) : 0;
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(gemv_fp8_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(gemv_fp8_kernel<NT>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     gemv_fp8_kernel<NT><<<grid, nwarps * 32, smem, stream>>>(p);
   };
   if (T <= 8) launch(std::integral_constant<int, 1>{});

@@ -24,7 +24,7 @@ __global__ void q_prep_kernel(const __nv_bfloat16* __restrict__ qb, long long qb
   const int pos = pos_of_tok[tok];
   const int half = rope / 2;
   const float* cs = cos_sin + (size_t)pos * rope;  // [cos(half) | sin(half)]
-  for (int h = warp; h < Hh; h += nw) {
+  for (int h = blockIdx.y * nw + warp; h < Hh; h += nw * gridDim.y) {
     const __nv_bfloat16* src = qb + (size_t)tok * qb_stride + (size_t)h * (nope + rope);
     // nope -> fp8, groups of 64; each lane handles nope/32 consecutive values
     if (qn_q) {
@@ -168,7 +168,7 @@ void q_prep(torch::Tensor qb, int64_t Hh, int64_t nope, int64_t rope, torch::Ten
   long long qcs = 0; int qhs = 0;
   if (qcat.has_value() && qcat->defined()) { qcs = qcat->stride(0); qhs = qcat->stride(1); }
   const int warps = std::min<int>(8, Hh);
-  q_prep_kernel<<<T, 32 * warps, 0, stream>>>((const __nv_bfloat16*)qb.data_ptr(), qb.stride(0), Hh, nope, rope,
+  q_prep_kernel<<<dim3(T, (Hh + warps - 1) / warps), 32 * warps, 0, stream>>>((const __nv_bfloat16*)qb.data_ptr(), qb.stride(0), Hh, nope, rope,
                                                pos_of_tok.data_ptr<int>(), cos_sin.data_ptr<float>(),
                                                (uint8_t*)opt_ptr(qn_q), (uint8_t*)opt_ptr(qn_s),
                                                (__nv_bfloat16*)opt_ptr(qcat), qcs, qhs, (int)rope_off,

@@ -138,6 +138,43 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, const float
 }
 
 // ---------------------------------------------------------------------------
+// Router logits: logits[t, e] = x[t, :] . W[e, :] with bf16 x and W, fp32 sums.
+// One warp per expert, 16-byte vector loads, 8 tokens per pass.
+__global__ void router_logits_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
+                                     const __nv_bfloat16* __restrict__ w, int E, float* __restrict__ out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (e >= E) return;
+  const __nv_bfloat16* wr = w + (size_t)e * H;
+  for (int t0 = 0; t0 < T; t0 += 8) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int k = lane * 8; k < H; k += 256) {
+      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr + k));
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv);
+      float wf[8];
+#pragma unroll
+      for (int i = 0; i < 4; i++) { const float2 f = __bfloat1622float2(w2[i]); wf[2 * i] = f.x; wf[2 * i + 1] = f.y; }
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        if (t0 + j >= T) break;
+        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + j) * H + k));
+        const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float2 f = __bfloat1622float2(x2[i]);
+          acc[j] = fmaf(f.x, wf[2 * i], fmaf(f.y, wf[2 * i + 1], acc[j]));
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const float v = warp_sum(acc[j]);
+      if (lane == 0 && t0 + j < T) out[(size_t)(t0 + j) * E + e] = v;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Pair-list builder.  outputs:
 //   sorted_tok[R]   token of each expert-sorted row
 //   pos_of[R]       routing r (= t*k + j) -> sorted row
@@ -158,14 +195,33 @@ __global__ void build_pairs_kernel(const int* __restrict__ topk_ids, int R, int 
     rank_scratch[r] = atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int s = 0, ps = 0;
-    for (int e = 0; e < E; e++) {
-      start[e] = s; pstart[e] = ps;
-      s += cnt[e];
-      ps += (cnt[e] + MB - 1) / MB;
+  // exclusive prefix sums of the row counts and pair counts (block scan, E <= 512)
+  {
+    __shared__ int wtot_c[32], wtot_p[32];
+    const int e = threadIdx.x, lane = e & 31, w = e >> 5;
+    const int c = e < E ? cnt[e] : 0, pc = (c + MB - 1) / MB;
+    int ic = c, ip = pc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a = __shfl_up_sync(0xffffffffu, ic, o), b = __shfl_up_sync(0xffffffffu, ip, o);
+      if (lane >= o) { ic += a; ip += b; }
     }
-    *n_pairs = ps;
+    if (lane == 31) { wtot_c[w] = ic; wtot_p[w] = ip; }
+    __syncthreads();
+    if (w == 0) {
+      const int nw = blockDim.x >> 5;
+      int tc = lane < nw ? wtot_c[lane] : 0, tp = lane < nw ? wtot_p[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, tc, o), b = __shfl_up_sync(0xffffffffu, tp, o);
+        if (lane >= o) { tc += a; tp += b; }
+      }
+      if (lane < nw) { wtot_c[lane] = tc; wtot_p[lane] = tp; }  // inclusive over warps
+    }
+    __syncthreads();
+    const int offc = w ? wtot_c[w - 1] : 0, offp = w ? wtot_p[w - 1] : 0;
+    if (e < E) { start[e] = offc + ic - c; pstart[e] = offp + ip - pc; }
+    if (e == E - 1) *n_pairs = offp + ip;
   }
   __syncthreads();
   for (int r = threadIdx.x; r < R; r += blockDim.x) {
@@ -200,6 +256,17 @@ void router_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_
       logits.data_ptr<float>(), bias.has_value() && bias->defined() ? bias->data_ptr<float>() : nullptr,
       T, E, (int)k, sigmoid ? 1 : 0, (int)n_group, (int)topk_group, norm ? 1 : 0, (float)scaling,
       ids.data_ptr<int>(), wts.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out) {
+  const int T = x.size(0), H = x.size(1), E = w.size(0);
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.is_contiguous() &&
+              w.is_contiguous() && H % 256 == 0, "router_logits: bf16 contiguous, H % 256 == 0");
+  if (T == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  router_logits_kernel<<<(E + 7) / 8, 256, 0, stream>>>((const __nv_bfloat16*)x.data_ptr(), T, H,
+                                                        (const __nv_bfloat16*)w.data_ptr(), E, out.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -13,34 +13,16 @@
 // * Each warp owns one 16-row block of W; every lane streams 8 bytes
 //   (32 codes) per 64-k chunk -- its MMA A-fragments for two k32 steps.
 // * Decode: the codes of byte pairs sit at 4-bit strides, so
-//   (w >> s) & 0x3333 is directly a prmt selector; one prmt over two
-//   4-entry e4m3 lookup words (k32 half a in the low word, half b in the
-//   high word, selected by bit 2 of each selector nibble) yields four e4m3
-//   weights.  11 ALU ops decode 16 weights.
-// * Scale folding: per row and 64-chunk the larger of the two block
-//   exponents E is factored out; each k32 block's weights are encoded as
-//   level * 2^(e - E) in e4m3 (exact down to 2^-9 relative; blocks more
-//   than 2^9 smaller than their neighbour contribute < 2^-9 of it and are
-//   flushed), so both MMAs accumulate into one fragment and the epilogue
-//   applies 2^E * a_scale once per chunk.
+//   (w >> s) & 0x3333 is directly a prmt selector; one prmt over the fixed
+//   4-entry e4m3 lookup word yields four e4m3 weights.
+// * Scales: each k32 MMA accumulates into its own fragment, and the UE8M0
+//   block scale (an exact power of two) and the activation scale are applied
+//   with FMAs, exactly as the format defines the dequantised weight.
 // * Misses (slot < 0) write zero rows and bump a miss counter.
 #include "common.cuh"
 #include "torch_glue.h"
 
 namespace moet {
-
-// lut[m] = e4m3 bytes of {-4,-1,+1,+4} * 2^-m, code order, little-endian.
-MOET_DEVICE uint8_t e4m3_pow2(int p, bool neg) {  // +-2^p as e4m3 (0 if underflow)
-  uint8_t b;
-  if (p >= -6) b = (uint8_t)((p + 7) << 3);
-  else if (p >= -9) b = (uint8_t)(1 << (p + 9));
-  else return 0;
-  return neg ? (uint8_t)(b | 0x80) : b;
-}
-MOET_DEVICE uint32_t code_lut_word(int m) {
-  return (uint32_t)e4m3_pow2(2 - m, true) | ((uint32_t)e4m3_pow2(-m, true) << 8) |
-         ((uint32_t)e4m3_pow2(-m, false) << 16) | ((uint32_t)e4m3_pow2(2 - m, false) << 24);
-}
 
 struct W2Args {
   const uint8_t* A; const uint8_t* sA; long long a_stride;  // activations (w2 layout), row stride bytes
@@ -54,10 +36,7 @@ struct W2Args {
 };
 
 template <int NT>
-__global__ void __launch_bounds__(128) moe_w2_gemv_kernel(W2Args p) {
-  __shared__ uint32_t lut[16];
-  if (threadIdx.x < 16) lut[threadIdx.x] = code_lut_word(threadIdx.x);
-  __syncthreads();
+__global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Args p) {
   const int pi = blockIdx.y;
   if (pi >= *p.n_pairs) return;
   const int4 pr = p.pairs[pi];
@@ -95,42 +74,60 @@ __global__ void __launch_bounds__(128) moe_w2_gemv_kernel(W2Args p) {
 #pragma unroll
   for (int i = 0; i < NT; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 
-#pragma unroll 4
-  for (int c = 0; c < KC; c++) {
-    const uint2 w = ldg_stream_u2(codes + (size_t)c * 256);
-    const uint8_t* s = sc + (size_t)c * 32;
-    const int ega = __ldg(s + g), eha = __ldg(s + g + 8), egb = __ldg(s + 16 + g), ehb = __ldg(s + 24 + g);
-    const int Eg = max(ega, egb), Eh = max(eha, ehb);
-    const uint32_t Lga = lut[min(Eg - ega, 15)], Lgb = lut[min(Eg - egb, 15)];
-    const uint32_t Lha = lut[min(Eh - eha, 15)], Lhb = lut[min(Eh - ehb, 15)];
-    const uint32_t lo = w.x, hi = w.y;
-    uint32_t A0[4], A1[4];
-    A0[0] = prmt(Lga, Lgb, lo & 0x3333u);
-    A0[1] = prmt(Lha, Lhb, hi & 0x3333u);
-    A0[2] = prmt(Lga, Lgb, (lo >> 2) & 0x3333u);
-    A0[3] = prmt(Lha, Lhb, (hi >> 2) & 0x3333u);
-    A1[0] = prmt(Lga, Lgb, ((lo >> 16) & 0x3333u) | 0x4444u);
-    A1[1] = prmt(Lha, Lhb, ((hi >> 16) & 0x3333u) | 0x4444u);
-    A1[2] = prmt(Lga, Lgb, ((lo >> 18) & 0x3333u) | 0x4444u);
-    A1[3] = prmt(Lha, Lhb, ((hi >> 18) & 0x3333u) | 0x4444u);
-    const float sg = ue8m0_to_float(Eg), sh = ue8m0_to_float(Eh);
+  // The warp's scale plane (16 rows x K/32 bytes, contiguous) -> shared memory.
+  extern __shared__ __align__(16) uint8_t scale_smem[];
+  uint8_t* ss = scale_smem + warp * 16 * KS;
+  for (int i = lane; i < KS; i += 32)
+    reinterpret_cast<uint4*>(ss)[i] = __ldg(reinterpret_cast<const uint4*>(sc) + i);
+  __syncwarp();
+
+  // Chunks are streamed in batches of U: all code loads of a batch are issued
+  // before any of them is consumed.  Decode uses one fixed lookup word (code ->
+  // e4m3 level), one prmt per 4 codes; each k32 MMA gets its own accumulator
+  // fragment and the two block scales are applied with FMAs.
+  constexpr uint32_t L = 0x4838B8C8u;   // e4m3 {-4, -1, +1, +4}
+  constexpr int U = 8;
+  for (int c0 = 0; c0 < KC; c0 += U) {
+    uint2 wv[U];
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-      uint2 xa = make_uint2(0, 0), xb = make_uint2(0, 0);
-      if (xr[nt] >= 0) {
-        const uint8_t* xp = xbase + (size_t)xr[nt] * p.a_stride + (size_t)c * 64;
-        xa = __ldg(reinterpret_cast<const uint2*>(xp));
-        xb = __ldg(reinterpret_cast<const uint2*>(xp + 32));
+    for (int u = 0; u < U; u++)
+      if (c0 + u < KC) wv[u] = ldg_stream_u2(codes + (size_t)(c0 + u) * 256);
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int c = c0 + u;
+      if (c >= KC) break;
+      const uint8_t* s = ss + c * 32;
+      const float sga = ue8m0_to_float(s[g]), sha = ue8m0_to_float(s[g + 8]);
+      const float sgb = ue8m0_to_float(s[16 + g]), shb = ue8m0_to_float(s[24 + g]);
+      const uint32_t lo = wv[u].x, hi = wv[u].y;
+      const uint32_t lo2 = lo >> 2, hi2 = hi >> 2, lo16 = lo >> 16, hi16 = hi >> 16, lo18 = lo >> 18, hi18 = hi >> 18;
+      uint32_t A0[4], A1[4];
+      A0[0] = prmt(L, L, lo & 0x3333u);
+      A0[1] = prmt(L, L, hi & 0x3333u);
+      A0[2] = prmt(L, L, lo2 & 0x3333u);
+      A0[3] = prmt(L, L, hi2 & 0x3333u);
+      A1[0] = prmt(L, L, lo16 & 0x3333u);
+      A1[1] = prmt(L, L, hi16 & 0x3333u);
+      A1[2] = prmt(L, L, lo18 & 0x3333u);
+      A1[3] = prmt(L, L, hi18 & 0x3333u);
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {
+        uint2 xa = make_uint2(0, 0), xb = make_uint2(0, 0);
+        if (xr[nt] >= 0) {
+          const uint8_t* xp = xbase + (size_t)xr[nt] * p.a_stride + (size_t)c * 64;
+          xa = __ldg(reinterpret_cast<const uint2*>(xp));
+          xb = __ldg(reinterpret_cast<const uint2*>(xp + 32));
+        }
+        float da[4] = {0.f, 0.f, 0.f, 0.f}, db[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_e4m3_16832(da, A0, xa.x, xa.y, da);
+        mma_e4m3_16832(db, A1, xb.x, xb.y, db);
+        const float as0 = sr0[nt] >= 0 ? ue8m0_to_float(__ldg(p.sA + (size_t)sr0[nt] * KC64 + c)) : 0.f;
+        const float as1 = sr1[nt] >= 0 ? ue8m0_to_float(__ldg(p.sA + (size_t)sr1[nt] * KC64 + c)) : 0.f;
+        acc[nt][0] = fmaf(fmaf(da[0], sga, db[0] * sgb), as0, acc[nt][0]);
+        acc[nt][1] = fmaf(fmaf(da[1], sga, db[1] * sgb), as1, acc[nt][1]);
+        acc[nt][2] = fmaf(fmaf(da[2], sha, db[2] * shb), as0, acc[nt][2]);
+        acc[nt][3] = fmaf(fmaf(da[3], sha, db[3] * shb), as1, acc[nt][3]);
       }
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      mma_e4m3_16832(d, A0, xa.x, xa.y, d);
-      mma_e4m3_16832(d, A1, xb.x, xb.y, d);
-      const float as0 = sr0[nt] >= 0 ? ue8m0_to_float(__ldg(p.sA + (size_t)sr0[nt] * KC64 + c)) : 0.f;
-      const float as1 = sr1[nt] >= 0 ? ue8m0_to_float(__ldg(p.sA + (size_t)sr1[nt] * KC64 + c)) : 0.f;
-      acc[nt][0] = fmaf(d[0], sg * as0, acc[nt][0]);
-      acc[nt][1] = fmaf(d[1], sg * as1, acc[nt][1]);
-      acc[nt][2] = fmaf(d[2], sh * as0, acc[nt][2]);
-      acc[nt][3] = fmaf(d[3], sh * as1, acc[nt][3]);
     }
   }
 #pragma unroll
@@ -158,7 +155,8 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int* __res
     w[threadIdx.x] = wts[tok * k + threadIdx.x];
   }
   __syncthreads();
-  for (int h = threadIdx.x * 4; h < H; h += blockDim.x * 4) {
+  const int h_begin = blockIdx.y * 1024, h_end = min(H, h_begin + 1024);
+  for (int h = h_begin + threadIdx.x * 4; h < h_end; h += blockDim.x * 4) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int j = 0; j < k; j++) {
       const float4 v = *reinterpret_cast<const float4*>(y + (size_t)pos[j] * H + h);
@@ -204,10 +202,12 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
   const int wpc = 4;
   dim3 grid((N / 16 + wpc - 1) / wpc, max_pairs);
   auto stream = at::cuda::getCurrentCUDAStream();
+  const size_t smem = (size_t)wpc * 16 * (K / 32);
+  TORCH_CHECK(smem <= 48 * 1024, "moe_w2_gemv: K too large for the shared scale stage");
   switch (rows_per_pair) {
-    case 8: moe_w2_gemv_kernel<1><<<grid, wpc * 32, 0, stream>>>(p); break;
-    case 16: moe_w2_gemv_kernel<2><<<grid, wpc * 32, 0, stream>>>(p); break;
-    case 32: moe_w2_gemv_kernel<4><<<grid, wpc * 32, 0, stream>>>(p); break;
+    case 8: moe_w2_gemv_kernel<1><<<grid, wpc * 32, smem, stream>>>(p); break;
+    case 16: moe_w2_gemv_kernel<2><<<grid, wpc * 32, smem, stream>>>(p); break;
+    case 32: moe_w2_gemv_kernel<4><<<grid, wpc * 32, smem, stream>>>(p); break;
     default: TORCH_CHECK(false, "moe_w2_gemv: rows_per_pair must be 8/16/32");
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -220,7 +220,7 @@ void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::
   TORCH_CHECK(H % 4 == 0 && k <= 32, "moe_combine: H % 4, k <= 32");
   if (T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  moe_combine_kernel<<<T, 256, 0, stream>>>(y.data_ptr<float>(), pos_of.data_ptr<int>(), wts.data_ptr<float>(), k, H,
+  moe_combine_kernel<<<dim3(T, (H + 1023) / 1024), 256, 0, stream>>>(y.data_ptr<float>(), pos_of.data_ptr<int>(), wts.data_ptr<float>(), k, H,
                                             (const __nv_bfloat16*)opt_ptr(resid), (const __nv_bfloat16*)opt_ptr(shared_out),
                                             (__nv_bfloat16*)opt_ptr(out), (float*)opt_ptr(out_f32));
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -91,9 +91,96 @@ __global__ void mtp_finalize_kernel(const int* __restrict__ targets, const int* 
   seq_pos[b] += a + 1;
 }
 
+// Split argmax (+ optional log-sum-exp): grid (rows, S).  Each block reduces
+// its slice to (max, argmax, sum exp(x - max)) in `part`; the last block of a
+// row (per-row arrival counter) merges the S partials and resets the counter,
+// so the kernel is replayable inside a CUDA graph.
+template <typename T>
+__global__ void argmax_split_kernel(const T* __restrict__ logits, long long stride, int V, int want_lse,
+                                    float* __restrict__ part, int* __restrict__ counter, int* __restrict__ ids,
+                                    float* __restrict__ lse, int* __restrict__ status) {
+  const int row = blockIdx.x, S = gridDim.y, sp = blockIdx.y;
+  const int per = (V + S - 1) / S, lo = sp * per, hi = min(V, lo + per);
+  const T* x = logits + (size_t)row * stride;
+  float bv = -INFINITY; int bi = 0x7fffffff;
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const float v = (float)x[i];
+    if (v > bv) { bv = v; bi = i; }
+  }
+  __shared__ float sv[32]; __shared__ int si[32]; __shared__ float ssum[32]; __shared__ int last;
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o); const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if (l == 0) { sv[w] = bv; si[w] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < nw; i++)
+      if (sv[i] > sv[0] || (sv[i] == sv[0] && si[i] < si[0])) { sv[0] = sv[i]; si[0] = si[i]; }
+  }
+  __syncthreads();
+  const float m = sv[0];
+  float sum = 0.f;
+  if (want_lse && m != -INFINITY) {
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) sum += __expf((float)x[i] - m);
+    sum = warp_sum(sum);
+    if (l == 0) ssum[w] = sum;
+    __syncthreads();
+    if (threadIdx.x == 0) { float t = 0.f; for (int i = 0; i < nw; i++) t += ssum[i]; sum = t; }
+  }
+  if (threadIdx.x == 0) {
+    float* pp = part + ((size_t)row * S + sp) * 3;
+    pp[0] = m; pp[1] = __int_as_float(si[0]); pp[2] = sum;
+    __threadfence();
+    last = atomicAdd(&counter[row], 1) == S - 1;
+  }
+  __syncthreads();
+  if (!last || threadIdx.x != 0) return;
+  __threadfence();
+  float M = -INFINITY; int I = 0x7fffffff;
+  for (int j = 0; j < S; j++) {
+    const volatile float* pp = part + ((size_t)row * S + j) * 3;
+    const float v = pp[0]; const int id = __float_as_int(pp[1]);
+    if (v > M || (v == M && id < I)) { M = v; I = id; }
+  }
+  if (want_lse) {
+    float tot = 0.f;
+    for (int j = 0; j < S; j++) {
+      const volatile float* pp = part + ((size_t)row * S + j) * 3;
+      if (pp[0] != -INFINITY) tot += __expf(pp[0] - M) * pp[2];
+    }
+    lse[row] = M + __logf(tot);
+  }
+  if (I < 0 || I >= V) { I = 0; set_status(status, kBadValue); }
+  ids[row] = I;
+  counter[row] = 0;
+}
+
 }  // namespace moet
 
 using namespace moet;
+
+void argmax_split(torch::Tensor logits, torch::Tensor ids, c10::optional<torch::Tensor> lse,
+                  c10::optional<torch::Tensor> status, torch::Tensor part, torch::Tensor counter) {
+  const int R = logits.size(0), V = logits.size(1);
+  TORCH_CHECK(logits.stride(1) == 1, "argmax_split: inner stride 1");
+  const int S = part.size(1);
+  TORCH_CHECK(part.size(0) >= R && part.size(2) == 3 && counter.numel() >= R, "argmax_split: scratch shapes");
+  if (R == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  dim3 grid(R, S);
+  const int want = lse.has_value() && lse->defined();
+  if (logits.scalar_type() == at::kFloat)
+    argmax_split_kernel<float><<<grid, 256, 0, stream>>>(logits.data_ptr<float>(), logits.stride(0), V, want,
+        part.data_ptr<float>(), counter.data_ptr<int>(), ids.data_ptr<int>(), (float*)opt_ptr(lse), (int*)opt_ptr(status));
+  else
+    argmax_split_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>((const __nv_bfloat16*)logits.data_ptr(),
+        logits.stride(0), V, want, part.data_ptr<float>(), counter.data_ptr<int>(), ids.data_ptr<int>(),
+        (float*)opt_ptr(lse), (int*)opt_ptr(status));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 
 void argmax_lse(torch::Tensor logits, torch::Tensor ids, c10::optional<torch::Tensor> lse,
                 c10::optional<torch::Tensor> maxv, c10::optional<torch::Tensor> status) {

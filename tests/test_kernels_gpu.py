@@ -373,3 +373,31 @@ def test_rmsnorm_quant_output_stride(C):
     assert torch.equal(q[:, :H], qa) and torch.equal(s[:, :H // 64], sa)
     C.rmsnorm_quant(b, None, None, w, 1e-6, None, qa, sa, None, None, 0)
     assert torch.equal(q[:, H:], qa) and torch.equal(s[:, H // 64:], sa)
+
+
+@pytest.mark.parametrize("T", [1, 3, 20])
+def test_router_logits(C, T):
+    g = torch.Generator().manual_seed(T)
+    E, H = 256, 4096
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16)
+    out = torch.empty(T, E, device=DEV)
+    C.router_logits(x.to(DEV), w.to(DEV), out)
+    assert rel(out.cpu(), x.float() @ w.float().t()) < 1e-5
+
+
+@pytest.mark.parametrize("R,V", [(1, 129280), (7, 4096), (3, 100)])
+def test_argmax_split_matches_torch_twice(C, R, V):
+    g = torch.Generator().manual_seed(R)
+    x = torch.randn(R, V, generator=g)
+    x[0, V // 3] = 9.0
+    x[-1, 5] = x[-1, 7] = 20.0   # tie -> lowest index
+    part = torch.empty(R, 32, 3, device=DEV)
+    cnt = torch.zeros(R, dtype=torch.int32, device=DEV)
+    for _ in range(2):   # counters reset themselves
+        ids = torch.empty(R, dtype=torch.int32, device=DEV)
+        lse = torch.empty(R, device=DEV)
+        C.argmax_split(x.to(DEV), ids, lse, None, part, cnt)
+        assert torch.equal(ids.cpu().long(), x.argmax(-1))
+        assert rel(lse.cpu(), torch.logsumexp(x, -1)) < 1e-5
+    assert int(cnt.abs().sum()) == 0

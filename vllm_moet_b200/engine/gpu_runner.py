@@ -53,6 +53,15 @@ class Workspace:
             self.bufs[(name, dtype)] = b
         return b[:n].view(*shape)
 
+    def zeros(self, name, shape, dtype):
+        """Like get(), but zero-initialised on first allocation (kernels keep it zero after use)."""
+        key = (name, dtype)
+        fresh = key not in self.bufs
+        t = self.get(name, shape, dtype)
+        if fresh:
+            self.bufs[key].zero_()
+        return t
+
 
 @dataclass
 class StepCtx:
@@ -102,7 +111,27 @@ class NativeRunner:
         return (self.ws.get(name + ".q", (T, K), torch.uint8), self.ws.get(name + ".s", (T, K // 64), torch.uint8))
 
     def _gemv(self, aq, as_, lin, out, resid=None):
-        self.C.gemv_fp8(aq, as_, lin.w, lin.s, out, resid)
+        """Dense FP8 linear: tcgen05 GEMM for prefill-sized token counts, the
+        weight-streaming GEMV for decode-sized ones."""
+        T, K = aq.shape[0], lin.w.shape[-1]
+        if T > 128 and K % 128 == 0 and lin.w.dim() == 2 and aq.stride(0) % 16 == 0:
+            self.C.tc_gemm_fp8(aq, as_, lin.w, lin.s, out, resid, 128, self.status)
+        else:
+            self.C.gemv_fp8(aq, as_, lin.w, lin.s, out, resid)
+
+    def _argmax(self, logits, ids):
+        R = logits.shape[0]
+        part = self.ws.get("argmax.part", (max(R, 1), 32, 3), torch.float32)
+        assert R <= 8192, "argmax rows"
+        cnt = self.ws.zeros("argmax.cnt", (8192,), torch.int32)
+        self.C.argmax_split(logits, ids, None, self.status, part, cnt)
+
+    def _router_w(self, lw):
+        w = getattr(lw, "_router_w_bf16", None)
+        if w is None:
+            w = lw.router_w.to(torch.bfloat16).contiguous()
+            lw._router_w_bf16 = w
+        return w
 
     def _tp_allreduce(self, t):
         if self.tp_group is not None:
@@ -130,7 +159,7 @@ class NativeRunner:
             C.q_prep(qb, Hh, nope, rope, ctx.pos, self.cos_sin, qnq, qns, qcat, lat, None)
             C.gemv_fp8(qnq.permute(1, 0, 2), qns.permute(1, 0, 2), lw.w_uk_t.w, lw.w_uk_t.s,
                        qcat[:, :, :lat].permute(1, 0, 2), None)
-            S = self.nsplit
+            S = max(1, min(32, 256 // T))
             opart = self.ws.get("opart", (S, T, Hh, lat), torch.float32)
             mlp = self.ws.get("mlpart", (S, T, Hh, 2), torch.float32)
             C.mla_decode(qcat, cache, ctx.block_table, ctx.seq, ctx.pos, opart, mlp, self.scale, self.status)
@@ -178,7 +207,10 @@ class NativeRunner:
         C.rmsnorm_quant(x, None, None, lw.ffn_norm, cfg.rms_eps, hb, hq, hs, h2q, h2s, 0)
         E, k = cfg.num_experts, cfg.top_k
         logits = self.ws.get("rlogits", (T, E), torch.float32)
-        torch.mm(hb.float(), lw.router_w.t(), out=logits)
+        if T <= 64:
+            C.router_logits(hb, self._router_w(lw), logits)
+        else:   # prefill: a plain GEMM, cuBLAS in fp32
+            torch.mm(hb.float(), lw.router_w.t(), out=logits)
         ids = self.ws.get("topk_ids", (T, k), torch.int32)
         wts = self.ws.get("topk_w", (T, k), torch.float32)
         C.router_topk(logits, lw.router_bias, k, cfg.router == "sigmoid", cfg.n_group, cfg.topk_group,
@@ -270,7 +302,7 @@ class NativeRunner:
         self._check(f"lm_head ({tag})", logits)
         return hid, logits
 
-    def _mtp(self, hidden, next_tokens, ctx: StepCtx):
+    def _mtp(self, hidden, next_tokens, ctx: StepCtx, rows=None):
         """MTP module over rows (h_i, token_{i+1}) -> (head-normed hidden, logits)."""
         cfg, C, m = self.cfg, self.C, self.mw.mtp
         T, H = ctx.T, cfg.hidden
@@ -284,6 +316,8 @@ class NativeRunner:
         self._gemv(ehq, ehs, m.eh_proj, xm)
         self._check("mtp eh_proj", xm)
         x = self._layer(m.layer, xm, ctx, self.kv[-1], 0)
+        if rows is not None:      # only these rows need the head (e.g. the last row of each prompt)
+            x = x[rows].contiguous()
         return self._final(x, None, "mtp")
 
     # ------------------------------------------------------------------ prefill
@@ -324,7 +358,7 @@ class NativeRunner:
         xl = x[last].contiguous()
         hid_last, logits = self._final(xl, None, "main")
         tgt = self.ws.get("pf.tgt", (len(prompts),), torch.int32)
-        C.argmax_lse(logits, tgt, None, None, self.status)
+        self._argmax(logits, tgt)
         B = len(prompts)
         if self.k == 0:
             state.set_rows(seq_rows, tgt, torch.tensor(lens, dtype=torch.int32, device=dev), None)
@@ -335,15 +369,12 @@ class NativeRunner:
         nxt = torch.empty_like(toks)
         nxt[:-1] = toks[1:]
         nxt[last] = tgt
-        mh, mlog = self._mtp(hid_all, nxt, ctx)
+        mh, ml = self._mtp(hid_all, nxt, ctx, rows=last)     # head only on the last row of each prompt
         drafts = torch.empty(B, self.k, dtype=torch.int32, device=dev)
-        d = self.ws.get("pf.d", (T,), torch.int32)
-        # only the last row of each prompt matters; argmax over those rows
-        ml = mlog[last].contiguous()
         d1 = self.ws.get("pf.d1", (B,), torch.int32)
-        C.argmax_lse(ml, d1, None, None, self.status)
+        self._argmax(ml, d1)
         drafts[:, 0] = d1
-        h_prev = mh[last].contiguous()
+        h_prev = mh.clone()
         cur_pos = torch.tensor(lens, dtype=torch.int32, device=dev)  # position of the first generated token
         prev_tok = d1
         for j in range(1, self.k):
@@ -353,7 +384,7 @@ class NativeRunner:
             ctx2 = StepCtx(T=B, pos=p2, seq=s2, slot=slot2, block_table=bt, mode="decode", mb=8)
             h_prev, lg = self._mtp(h_prev.clone(), prev_tok, ctx2)
             dj = self.ws.get("pf.dj", (B,), torch.int32)
-            C.argmax_lse(lg, dj, None, None, self.status)
+            self._argmax(lg, dj)
             drafts[:, j] = dj
             prev_tok = dj.clone()
         state.set_rows(seq_rows, tgt, cur_pos, drafts)
@@ -390,7 +421,7 @@ class NativeRunner:
                       mb=8 if T * self.cfg.top_k <= 256 else 16)
         x = self._main(st.tokens.view(-1), ctx)
         hid, logits = self._final(x, None, "main")
-        C.argmax_lse(logits, st.targets.view(-1), None, None, self.status)
+        self._argmax(logits, st.targets.view(-1))
         C.mtp_accept(st.targets, st.tokens, st.out_tokens, st.n_acc, st.active)
         if k == 0:
             st.seq_pos.add_(st.active)
@@ -399,7 +430,7 @@ class NativeRunner:
         # MTP pass 1 over the verify rows: (h_j, target_j) at position p + j
         mh, mlog = self._mtp(hid, st.targets.view(-1), ctx)
         am = self.ws.get("dec.am", (T,), torch.int32)
-        C.argmax_lse(mlog, am, None, None, self.status)
+        self._argmax(mlog, am)
         sel = (st.arange_b * kp1 + st.n_acc).long()
         prev_tok = am[sel]
         st.drafts[:, 0] = prev_tok
@@ -413,7 +444,7 @@ class NativeRunner:
                            mode="decode", mb=8)
             h_prev, lg = self._mtp(h_prev, prev_tok, ctx2)
             dj = self.ws.get("dec.dj", (B,), torch.int32)
-            C.argmax_lse(lg, dj, None, None, self.status)
+            self._argmax(lg, dj)
             st.drafts[:, j] = dj
             prev_tok = dj
         C.mtp_finalize(st.targets, st.n_acc, st.drafts, st.tokens, st.seq_pos, st.active)

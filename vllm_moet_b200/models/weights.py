@@ -287,7 +287,7 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
         lw.down = lin((H, I))
         return lw
     E, I = cfg.num_experts, cfg.moe_intermediate // tp_size
-    lw.router_w = rng.normal((E, H))
+    lw.router_w = rng.normal((E, H)).to(torch.bfloat16).float()   # bf16-valued gate weights
     lw.router_bias = torch.zeros(E, dtype=torch.float32, device=dev)
     Is = cfg.moe_intermediate * cfg.num_shared_experts // tp_size
     if cfg.num_shared_experts:
