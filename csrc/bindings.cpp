@@ -22,6 +22,11 @@ void build_pairs(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor ra
 void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out);
 void argmax_split(torch::Tensor logits, torch::Tensor ids, c10::optional<torch::Tensor> lse,
                   c10::optional<torch::Tensor> status, torch::Tensor part, torch::Tensor counter);
+void build_pairs_padded(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor rank_scratch,
+                        torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
+                        torch::Tensor n_rows, torch::Tensor status);
+void gather_rows(torch::Tensor src_q, torch::Tensor src_s, torch::Tensor idx, torch::Tensor n_rows, torch::Tensor dst_q,
+                 torch::Tensor dst_s);
 // moe_w2.cu
 void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor> gather, torch::Tensor pairs,
                  torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
@@ -73,6 +78,13 @@ void tc_moe_w2(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor> g
 void tc_gemm_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tensor sw, torch::Tensor out,
                  c10::optional<torch::Tensor> resid, int64_t nt, torch::Tensor status);
 
+void ws_moe_w2(torch::Tensor a, torch::Tensor sa, torch::Tensor pairs, torch::Tensor n_pairs, torch::Tensor pool,
+               int64_t codes_off, int64_t scale_off, torch::Tensor slot_table, torch::Tensor out, int64_t N,
+               int64_t K, int64_t nt, c10::optional<torch::Tensor> miss_count, torch::Tensor status,
+               c10::optional<torch::Tensor> dbg_clk);
+void ws_gemm_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tensor sw, torch::Tensor out,
+                 c10::optional<torch::Tensor> resid, int64_t T, torch::Tensor status);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vllm_moet_b200 sm_100a kernels";
   m.def("rmsnorm_quant", &rmsnorm_quant);
@@ -81,10 +93,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_fp8", &gemv_fp8);
   m.def("router_topk", &router_topk);
   m.def("build_pairs", &build_pairs);
+  m.def("build_pairs_padded", &build_pairs_padded);
+  m.def("gather_rows", &gather_rows);
   m.def("router_logits", &router_logits);
   m.def("tc_gemm_test", &tc_gemm_test);
   m.def("tc_moe_w2", &tc_moe_w2);
   m.def("tc_gemm_fp8", &tc_gemm_fp8);
+  m.def("ws_moe_w2", &ws_moe_w2);
+  m.def("ws_gemm_fp8", &ws_gemm_fp8);
   m.def("argmax_split", &argmax_split);
   m.def("moe_w2_gemv", &moe_w2_gemv);
   m.def("moe_combine", &moe_combine);

@@ -183,7 +183,8 @@ __global__ void router_logits_kernel(const __nv_bfloat16* __restrict__ x, int T,
 __global__ void build_pairs_kernel(const int* __restrict__ topk_ids, int R, int k, int E, int MB,
                                    int* __restrict__ rank_scratch, int* __restrict__ sorted_tok,
                                    int* __restrict__ pos_of, int4* __restrict__ pairs,
-                                   int* __restrict__ n_pairs, int* __restrict__ status) {
+                                   int* __restrict__ n_pairs, int* __restrict__ status,
+                                   int pad = 0, int* __restrict__ n_rows = nullptr) {
   __shared__ int cnt[kMaxE];
   __shared__ int start[kMaxE];
   __shared__ int pstart[kMaxE];
@@ -199,7 +200,8 @@ __global__ void build_pairs_kernel(const int* __restrict__ topk_ids, int R, int 
   {
     __shared__ int wtot_c[32], wtot_p[32];
     const int e = threadIdx.x, lane = e & 31, w = e >> 5;
-    const int c = e < E ? cnt[e] : 0, pc = (c + MB - 1) / MB;
+    const int c0 = e < E ? cnt[e] : 0, pc = (c0 + MB - 1) / MB;
+    const int c = pad ? pc * MB : c0;          // padded: every segment starts at a multiple of MB
     int ic = c, ip = pc;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -221,7 +223,7 @@ __global__ void build_pairs_kernel(const int* __restrict__ topk_ids, int R, int 
     __syncthreads();
     const int offc = w ? wtot_c[w - 1] : 0, offp = w ? wtot_p[w - 1] : 0;
     if (e < E) { start[e] = offc + ic - c; pstart[e] = offp + ip - pc; }
-    if (e == E - 1) *n_pairs = offp + ip;
+    if (e == E - 1) { *n_pairs = offp + ip; if (n_rows) *n_rows = offc + ic; }
   }
   __syncthreads();
   for (int r = threadIdx.x; r < R; r += blockDim.x) {
@@ -235,6 +237,8 @@ __global__ void build_pairs_kernel(const int* __restrict__ topk_ids, int R, int 
     const int c = cnt[e];
     for (int i = 0; i * MB < c; i++)
       pairs[pstart[e] + i] = make_int4(e, start[e] + i * MB, min(MB, c - i * MB), 0);
+    if (pad)   // padding rows of the segment map to no token
+      for (int i = c; i < (c + MB - 1) / MB * MB; i++) sorted_tok[start[e] + i] = -1;
   }
 }
 
@@ -259,6 +263,36 @@ void router_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// dst[r] = src[idx[r]] (rows of e4m3 + their per-64 scales); idx < 0 -> zeros; rows >= *n_rows untouched.
+__global__ void gather_rows_kernel(const uint8_t* __restrict__ src_q, const uint8_t* __restrict__ src_s, int K,
+                                   long long src_stride, const int* __restrict__ idx, const int* __restrict__ n_rows,
+                                   uint8_t* __restrict__ dst_q, uint8_t* __restrict__ dst_s, long long dst_stride) {
+  const int r = blockIdx.x;
+  if (r >= *n_rows) return;
+  const int i = idx[r];
+  const int nv = K / 16;
+  for (int c = threadIdx.x; c < nv; c += blockDim.x) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (i >= 0) v = __ldg(reinterpret_cast<const uint4*>(src_q + (size_t)i * src_stride) + c);
+    reinterpret_cast<uint4*>(dst_q + (size_t)r * dst_stride)[c] = v;
+  }
+  for (int c = threadIdx.x; c < K / 64; c += blockDim.x)
+    dst_s[(size_t)r * (K / 64) + c] = i >= 0 ? src_s[(size_t)i * (K / 64) + c] : 0;
+}
+
+void gather_rows(torch::Tensor src_q, torch::Tensor src_s, torch::Tensor idx, torch::Tensor n_rows, torch::Tensor dst_q,
+                 torch::Tensor dst_s) {
+  const int K = src_q.size(1), R = idx.size(0);
+  TORCH_CHECK(K % 64 == 0 && src_q.stride(0) % 16 == 0 && dst_q.stride(0) % 16 == 0, "gather_rows: alignment");
+  TORCH_CHECK(dst_q.size(0) >= R && dst_s.size(0) >= R, "gather_rows: destination too small");
+  if (R == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  gather_rows_kernel<<<R, 128, 0, stream>>>((const uint8_t*)src_q.data_ptr(), (const uint8_t*)src_s.data_ptr(), K,
+                                            src_q.stride(0), idx.data_ptr<int>(), n_rows.data_ptr<int>(),
+                                            (uint8_t*)dst_q.data_ptr(), (uint8_t*)dst_s.data_ptr(), dst_q.stride(0));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out) {
   const int T = x.size(0), H = x.size(1), E = w.size(0);
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.is_contiguous() &&
@@ -267,6 +301,24 @@ void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out) {
   auto stream = at::cuda::getCurrentCUDAStream();
   router_logits_kernel<<<(E + 7) / 8, 256, 0, stream>>>((const __nv_bfloat16*)x.data_ptr(), T, H,
                                                         (const __nv_bfloat16*)w.data_ptr(), E, out.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Padded variant: each expert's segment of the sorted rows starts at a multiple of MB
+// (so a pair's rows are MB-aligned and contiguous); total rows -> n_rows[0].
+// sorted_tok / pos_of must hold R / MB * MB + min(E, R) * MB rows.
+void build_pairs_padded(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor rank_scratch,
+                        torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
+                        torch::Tensor n_rows, torch::Tensor status) {
+  const int T = topk_ids.size(0), k = topk_ids.size(1), R = T * k;
+  TORCH_CHECK(E <= kMaxE, "build_pairs_padded: E <= 512");
+  const int64_t P = R / MB + std::min<int64_t>(E, R);
+  TORCH_CHECK(pairs.size(0) >= P && sorted_tok.size(0) >= P * MB, "build_pairs_padded: buffers too small");
+  auto stream = at::cuda::getCurrentCUDAStream();
+  build_pairs_kernel<<<1, 1024, 0, stream>>>(topk_ids.data_ptr<int>(), R, k, (int)E, (int)MB,
+                                             rank_scratch.data_ptr<int>(), sorted_tok.data_ptr<int>(),
+                                             pos_of.data_ptr<int>(), (int4*)pairs.data_ptr<int>(),
+                                             n_pairs.data_ptr<int>(), status.data_ptr<int>(), 1, n_rows.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

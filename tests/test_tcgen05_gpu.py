@@ -91,3 +91,73 @@ def test_tc_gemm_fp8(C, T, N, K, NT):
     outb = torch.empty(T, N, dtype=torch.bfloat16, device=DEV)
     C.tc_gemm_fp8(a.to(DEV), sa.to(DEV), w.to(DEV), sw.to(DEV), outb, res, NT, st)
     assert rel(outb.cpu().float(), (A @ Wd.t()).float() + res.cpu().float()) < 1e-2
+
+
+@pytest.mark.parametrize("T,k,E,N,K,NT", [(1, 8, 16, 128, 256, 8), (3, 8, 32, 256, 1536, 8), (20, 4, 8, 384, 512, 16),
+                                          (40, 8, 16, 128, 4096, 16), (300, 8, 16, 256, 512, 128)])
+def test_ws_moe_w2_padded(C, T, k, E, N, K, NT):
+    g = torch.Generator().manual_seed(T * 11 + N)
+    codes = torch.randint(0, 4, (E, N, K), generator=g, dtype=torch.uint8)
+    sc = torch.randint(118, 132, (E, N, K // 32), generator=g, dtype=torch.uint8)
+    pool = torch.stack([torch.cat([planes.pack_codes(codes[e]), planes.pack_scales(sc[e])]) for e in range(E)]).to(DEV)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).int().to(DEV)
+    R = T * k
+    P = R // NT + min(E, R)
+    Rp = P * NT
+    rank = torch.empty(R, dtype=torch.int32, device=DEV)
+    stok = torch.empty(Rp, dtype=torch.int32, device=DEV)
+    posof = torch.empty(R, dtype=torch.int32, device=DEV)
+    pairs = torch.empty(P, 4, dtype=torch.int32, device=DEV)
+    npairs = torch.zeros(1, dtype=torch.int32, device=DEV); nrows = torch.zeros(1, dtype=torch.int32, device=DEV)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    C.build_pairs_padded(ids, E, NT, rank, stok, posof, pairs, npairs, nrows, st)
+    assert int(nrows) % NT == 0 and int(nrows) <= Rp
+    pr = pairs[: int(npairs)].cpu()
+    assert (pr[:, 1] % NT == 0).all()
+    x = torch.randn(T, K, generator=g)
+    q, s = fp8.quant_act_fp8(x)
+    qw2 = fp8.to_w2_layout(q.view(torch.uint8)).to(DEV)
+    aq = torch.empty(Rp, K, dtype=torch.uint8, device=DEV); as_ = torch.empty(Rp, K // 64, dtype=torch.uint8, device=DEV)
+    C.gather_rows(qw2, s.to(DEV), stok, nrows, aq, as_)
+    out = torch.full((Rp, N), float("nan"), device=DEV)
+    slots = torch.arange(E, dtype=torch.int32, device=DEV)
+    slots[int(ids[0, 0])] = -1           # one missing expert -> zero rows + miss count
+    miss = torch.zeros(1, dtype=torch.int32, device=DEV)
+    for _ in range(2):
+        C.ws_moe_w2(aq, as_, pairs, npairs, pool, 0, N * K // 4, slots, out, N, K, NT, miss, st, None)
+    torch.cuda.synchronize()
+    assert int(st) == 0 and int(miss) >= 1
+    A = fp8.dequant_act_fp8(q, s).double()
+    po = posof.cpu().long()
+    ids_c = ids.cpu()
+    for tt in range(T):
+        for j in range(k):
+            e = int(ids_c[tt, j])
+            got = out[po[tt * k + j]].cpu()
+            if e == int(ids_c[0, 0]):
+                assert (got == 0).all()
+                continue
+            W = codebook.dequant_codes(codes[e], sc[e]).double()
+            assert rel(got, A[tt] @ W.t()) < 1e-4, (tt, j)
+
+
+@pytest.mark.parametrize("T,N,K", [(1, 128, 128), (130, 384, 512), (300, 200, 1024), (256, 4096, 4096)])
+def test_ws_gemm_fp8(C, T, N, K):
+    g = torch.Generator().manual_seed(T + N + K)
+    Tp = (T + 127) // 128 * 128
+    a = torch.zeros(Tp, K, dtype=torch.uint8)
+    a[:T] = (torch.randn(T, K, generator=g) * 2).to(torch.float8_e4m3fn).view(torch.uint8)
+    sap = torch.full((Tp, K // 64), 127, dtype=torch.uint8)
+    sap[:T] = torch.randint(120, 134, (T, K // 64), generator=g, dtype=torch.uint8)
+    sa = sap[:T]
+    w = (torch.randn(N, K, generator=g) * 2).to(torch.float8_e4m3fn).view(torch.uint8)
+    sw = torch.randint(118, 130, ((N + 127) // 128, K // 128), generator=g, dtype=torch.uint8)
+    out = torch.empty(T, N, device=DEV)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ad = a.to(DEV)
+    C.ws_gemm_fp8(ad, sap.to(DEV), w.to(DEV), sw.to(DEV), out, None, T, st)
+    torch.cuda.synchronize()
+    A = fp8.dequant_act_fp8(a[:T].view(torch.float8_e4m3fn), sa).double()
+    Wd = w.view(torch.float8_e4m3fn).double() * torch.exp2(sw.double() - 127).repeat_interleave(128, 0)[:N].repeat_interleave(128, 1)
+    assert int(st) == 0
+    assert rel(out.cpu(), A @ Wd.t()) < 1e-4

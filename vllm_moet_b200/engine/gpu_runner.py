@@ -107,13 +107,39 @@ class NativeRunner:
         self.debug_finite = os.environ.get("MOET_DEBUG_FINITE", "0") == "1"
 
     # ------------------------------------------------------------------ helpers
+    @staticmethod
+    def _pad128(T):
+        return (T + 127) // 128 * 128
+
     def _fp8(self, name, T, K):
-        return (self.ws.get(name + ".q", (T, K), torch.uint8), self.ws.get(name + ".s", (T, K // 64), torch.uint8))
+        """FP8 activation buffers; rows are allocated in multiples of 128 so the
+        tensor-core GEMM can read whole 128-row TMA boxes (callers see [:T])."""
+        Tp = self._pad128(T) if T > 128 else T
+        q = self.ws.get(name + ".q", (Tp, K), torch.uint8)
+        s = self.ws.get(name + ".s", (Tp, K // 64), torch.uint8)
+        return q[:T], s[:T]
+
+    @staticmethod
+    def _padded_view(t, rows):
+        """The 128-row padded parent of a [:T] view made by _fp8, or None."""
+        if not t.is_contiguous():
+            return None
+        need = rows * t.shape[1] * t.element_size()
+        if t.untyped_storage().nbytes() - t.storage_offset() * t.element_size() < need:
+            return None
+        return t.as_strided((rows, t.shape[1]), t.stride())
 
     def _gemv(self, aq, as_, lin, out, resid=None):
-        """Dense FP8 linear: tcgen05 GEMM for prefill-sized token counts, the
-        weight-streaming GEMV for decode-sized ones."""
+        """Dense FP8 linear: the warp-specialized tcgen05 GEMM for prefill-sized
+        token counts, the weight-streaming GEMV for decode-sized ones."""
         T, K = aq.shape[0], lin.w.shape[-1]
+        N = lin.w.shape[0]
+        if T > 128 and K % 128 == 0 and lin.w.dim() == 2 and N % 8 == 0:
+            Tp = self._pad128(T)
+            ap, sp = self._padded_view(aq, Tp), self._padded_view(as_, Tp)
+            if ap is not None and sp is not None:
+                self.C.ws_gemm_fp8(ap, sp, lin.w, lin.s, out, resid, T, self.status)
+                return
         if T > 128 and K % 128 == 0 and lin.w.dim() == 2 and aq.stride(0) % 16 == 0:
             self.C.tc_gemm_fp8(aq, as_, lin.w, lin.s, out, resid, 128, self.status)
         else:
@@ -216,25 +242,13 @@ class NativeRunner:
         C.router_topk(logits, lw.router_bias, k, cfg.router == "sigmoid", cfg.n_group, cfg.topk_group,
                       cfg.norm_topk_prob, cfg.routed_scaling, ids, wts)
         R = T * k
-        MB = ctx.mb
-        P = R // MB + min(E, R)
-        rank = self.ws.get("rank", (R,), torch.int32)
-        stok = self.ws.get("stok", (R,), torch.int32)
-        posof = self.ws.get("posof", (R,), torch.int32)
-        pairs = self.ws.get("pairs", (P, 4), torch.int32)
-        npairs = self.ws.get("npairs", (1,), torch.int32)
-        C.build_pairs(ids, E, MB, rank, stok, posof, pairs, npairs, self.status)
         ex = lw.experts
         L = ex.layout
         I = L.I
-        c13 = self.ws.get("c13", (R, 2 * I), torch.float32)
-        C.moe_w2_gemv(h2q, h2s, stok, pairs, npairs, ex.pool, L.off_codes13, L.off_sc13, ex.slot_table, c13,
-                      2 * I, H, MB, self.miss)
-        a2q, a2s = self._fp8("a2", R, I)
-        C.swiglu_quant(c13, cfg.swiglu_limit or 0.0, None, 1, a2q, a2s)
-        y2 = self.ws.get("y2", (R, H), torch.float32)
-        C.moe_w2_gemv(a2q, a2s, None, pairs, npairs, ex.pool, L.off_codes2, L.off_sc2, ex.slot_table, y2,
-                      H, I, MB, self.miss)
+        if ctx.mode == "prefill" and H % 128 == 0 and I % 128 == 0 and (2 * I) % 128 == 0:
+            y2, posof = self._moe_tc(h2q, h2s, ids, ex, R, T)
+        else:
+            y2, posof = self._moe_gemv(h2q, h2s, ids, ex, R, ctx.mb)
         sh = None
         if lw.shared_gate_up is not None:
             Is2 = lw.shared_gate_up.w.shape[0]
@@ -251,6 +265,60 @@ class NativeRunner:
             C.moe_combine(y2, posof, wts, None, sh, part, None)
             self._tp_allreduce(part)
             torch.add(x, part, out=out)
+
+    def _moe_tc(self, h2q, h2s, ids, ex, R, T):
+        """Prefill experts on tensor cores: 128-row expert-aligned pairs, activations
+        gathered into expert order, two warp-specialized tcgen05 GEMMs."""
+        C, cfg = self.C, self.cfg
+        E, H = cfg.num_experts, cfg.hidden
+        L = ex.layout
+        I = L.I
+        MB = 128
+        P = R // MB + min(E, R)
+        Rp = P * MB
+        rank = self.ws.get("rank", (R,), torch.int32)
+        stok = self.ws.get("stok_p", (Rp,), torch.int32)
+        posof = self.ws.get("posof", (R,), torch.int32)
+        pairs = self.ws.get("pairs", (P, 4), torch.int32)
+        npairs = self.ws.get("npairs", (1,), torch.int32)
+        nrows = self.ws.get("nrows", (1,), torch.int32)
+        C.build_pairs_padded(ids, E, MB, rank, stok, posof, pairs, npairs, nrows, self.status)
+        xq = self.ws.get("xs.q", (Rp, H), torch.uint8)
+        xs = self.ws.get("xs.s", (Rp, H // 64), torch.uint8)
+        C.gather_rows(h2q, h2s, stok, nrows, xq, xs)
+        c13 = self.ws.get("c13", (Rp, 2 * I), torch.float32)
+        C.ws_moe_w2(xq, xs, pairs, npairs, ex.pool, L.off_codes13, L.off_sc13, ex.slot_table, c13, 2 * I, H, MB,
+                    self.miss, self.status, None)
+        a2q = self.ws.get("a2p.q", (Rp, I), torch.uint8)
+        a2s = self.ws.get("a2p.s", (Rp, I // 64), torch.uint8)
+        C.swiglu_quant(c13, cfg.swiglu_limit or 0.0, nrows, 1, a2q, a2s)
+        y2 = self.ws.get("y2", (Rp, H), torch.float32)
+        C.ws_moe_w2(a2q, a2s, pairs, npairs, ex.pool, L.off_codes2, L.off_sc2, ex.slot_table, y2, H, I, MB,
+                    self.miss, self.status, None)
+        return y2, posof
+
+    def _moe_gemv(self, h2q, h2s, ids, ex, R, MB):
+        """Decode experts: mma.sync weight-streaming GEMV over the compact pair list."""
+        C, cfg = self.C, self.cfg
+        E, H = cfg.num_experts, cfg.hidden
+        L = ex.layout
+        I = L.I
+        P = R // MB + min(E, R)
+        rank = self.ws.get("rank", (R,), torch.int32)
+        stok = self.ws.get("stok", (R,), torch.int32)
+        posof = self.ws.get("posof", (R,), torch.int32)
+        pairs = self.ws.get("pairs", (P, 4), torch.int32)
+        npairs = self.ws.get("npairs", (1,), torch.int32)
+        C.build_pairs(ids, E, MB, rank, stok, posof, pairs, npairs, self.status)
+        c13 = self.ws.get("c13", (R, 2 * I), torch.float32)
+        C.moe_w2_gemv(h2q, h2s, stok, pairs, npairs, ex.pool, L.off_codes13, L.off_sc13, ex.slot_table, c13,
+                      2 * I, H, MB, self.miss)
+        a2q, a2s = self._fp8("a2", R, I)
+        C.swiglu_quant(c13, cfg.swiglu_limit or 0.0, None, 1, a2q, a2s)
+        y2 = self.ws.get("y2", (R, H), torch.float32)
+        C.moe_w2_gemv(a2q, a2s, None, pairs, npairs, ex.pool, L.off_codes2, L.off_sc2, ex.slot_table, y2,
+                      H, I, MB, self.miss)
+        return y2, posof
 
     def _ffn_out(self, lin, aq, as_, x, out, T):
         if self.tp_group is None:
@@ -307,8 +375,7 @@ class NativeRunner:
         cfg, C, m = self.cfg, self.C, self.mw.mtp
         T, H = ctx.T, cfg.hidden
         emb = torch.nn.functional.embedding(next_tokens.long(), self.mw.embed)
-        ehq = self.ws.get("eh.q", (T, 2 * H), torch.uint8)
-        ehs = self.ws.get("eh.s", (T, 2 * H // 64), torch.uint8)
+        ehq, ehs = self._fp8("eh", T, 2 * H)
         C.rmsnorm_quant(emb, None, None, m.enorm, cfg.rms_eps, None, ehq, ehs, None, None, 2 * H)
         C.rmsnorm_quant(hidden, None, None, m.hnorm, cfg.rms_eps, None, ehq[:, H:], ehs[:, H // 64:], None, None,
                         2 * H)
