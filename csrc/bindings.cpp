@@ -5,13 +5,14 @@
 void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> add, c10::optional<torch::Tensor> x_out,
                    torch::Tensor w, double eps, c10::optional<torch::Tensor> y_out,
                    c10::optional<torch::Tensor> q0, c10::optional<torch::Tensor> s0,
-                   c10::optional<torch::Tensor> q1, c10::optional<torch::Tensor> s1, int64_t ostride);
+                   c10::optional<torch::Tensor> q1, c10::optional<torch::Tensor> s1, int64_t ostride,
+                   c10::optional<torch::Tensor> ar);
 void swiglu_quant(torch::Tensor in, double limit, c10::optional<torch::Tensor> n_rows, int64_t layout,
                   torch::Tensor q, torch::Tensor s);
 void quant_fp8(torch::Tensor x, int64_t layout, torch::Tensor q, torch::Tensor s);
 // gemv_fp8.cu
 void gemv_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tensor sw, torch::Tensor out,
-              c10::optional<torch::Tensor> resid);
+              c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> ar);
 // moe_route.cu
 void router_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_t k, bool sigmoid,
                  int64_t n_group, int64_t topk_group, bool norm, double scaling, torch::Tensor ids,
@@ -20,8 +21,10 @@ void build_pairs(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor ra
                  torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
                  torch::Tensor status);
 void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out);
-void argmax_split(torch::Tensor logits, torch::Tensor ids, c10::optional<torch::Tensor> lse,
-                  c10::optional<torch::Tensor> status, torch::Tensor part, torch::Tensor counter);
+void argmax_split(torch::Tensor logits, c10::optional<torch::Tensor> ids, c10::optional<torch::Tensor> lse,
+                  c10::optional<torch::Tensor> status, torch::Tensor part, torch::Tensor counter,
+                  c10::optional<torch::Tensor> mv, int64_t id_offset);
+void argmax_merge(torch::Tensor parts, torch::Tensor ids);
 void build_pairs_padded(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor rank_scratch,
                         torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
                         torch::Tensor n_rows, torch::Tensor status);
@@ -34,7 +37,14 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
                  c10::optional<torch::Tensor> miss_count);
 void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::optional<torch::Tensor> resid,
                  c10::optional<torch::Tensor> shared_out, c10::optional<torch::Tensor> out,
-                 c10::optional<torch::Tensor> out_f32);
+                 c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> ar);
+// symm.cu
+std::tuple<int64_t, at::Tensor> symm_alloc(int64_t bytes);
+int64_t symm_open(at::Tensor handle);
+void symm_close(int64_t ptr);
+void symm_free(int64_t ptr);
+at::Tensor symm_view(int64_t ptr, int64_t bytes, int64_t device);
+void ar_test(at::Tensor desc, at::Tensor x, c10::optional<at::Tensor> resid, at::Tensor out, int64_t mode);
 
 // mla_decode.cu
 void mla_decode(torch::Tensor q, torch::Tensor kv, torch::Tensor block_table, torch::Tensor seq_of_tok,
@@ -87,10 +97,13 @@ void ws_gemm_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tens
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vllm_moet_b200 sm_100a kernels";
-  m.def("rmsnorm_quant", &rmsnorm_quant);
+  m.def("rmsnorm_quant", &rmsnorm_quant, py::arg("x"), py::arg("add"), py::arg("x_out"), py::arg("w"), py::arg("eps"),
+        py::arg("y_out"), py::arg("q0"), py::arg("s0"), py::arg("q1"), py::arg("s1"), py::arg("ostride"),
+        py::arg("ar") = py::none());
   m.def("swiglu_quant", &swiglu_quant);
   m.def("quant_fp8", &quant_fp8);
-  m.def("gemv_fp8", &gemv_fp8);
+  m.def("gemv_fp8", &gemv_fp8, py::arg("a"), py::arg("sa"), py::arg("w"), py::arg("sw"), py::arg("out"),
+        py::arg("resid"), py::arg("ar") = py::none());
   m.def("router_topk", &router_topk);
   m.def("build_pairs", &build_pairs);
   m.def("build_pairs_padded", &build_pairs_padded);
@@ -101,9 +114,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_gemm_fp8", &tc_gemm_fp8);
   m.def("ws_moe_w2", &ws_moe_w2);
   m.def("ws_gemm_fp8", &ws_gemm_fp8);
-  m.def("argmax_split", &argmax_split);
+  m.def("argmax_split", &argmax_split, py::arg("logits"), py::arg("ids"), py::arg("lse"), py::arg("status"),
+        py::arg("part"), py::arg("counter"), py::arg("mv") = py::none(), py::arg("id_offset") = 0);
+  m.def("argmax_merge", &argmax_merge);
   m.def("moe_w2_gemv", &moe_w2_gemv);
-  m.def("moe_combine", &moe_combine);
+  m.def("moe_combine", &moe_combine, py::arg("y"), py::arg("pos_of"), py::arg("wts"), py::arg("resid"),
+        py::arg("shared_out"), py::arg("out"), py::arg("out_f32"), py::arg("ar") = py::none());
+  m.def("symm_alloc", &symm_alloc);
+  m.def("symm_open", &symm_open);
+  m.def("symm_close", &symm_close);
+  m.def("symm_free", &symm_free);
+  m.def("symm_view", &symm_view);
+  m.def("ar_test", &ar_test);
   m.def("mla_decode", &mla_decode);
   m.def("mla_combine", &mla_combine);
   m.def("q_prep", &q_prep);

@@ -13,6 +13,7 @@
 //   MMA 0 uses bytes 0..7, MMA 1 bytes 8..15.
 // Optional batch dimension (blockIdx.z) for per-head weights (MLA absorb).
 #include "common.cuh"
+#include "symm.cuh"
 #include "torch_glue.h"
 
 namespace moet {
@@ -27,6 +28,8 @@ struct GemvArgs {
   long long out_row_stride, out_batch_stride; // elements
   int sw_cols;                                // K/128 (ceil)
   int out_f32;
+  int ar_on;                                  // push fp32 partials to every TP peer instead of writing out
+  ArDesc ar;
 };
 
 template <int NT>
@@ -111,6 +114,21 @@ __global__ void __launch_bounds__(256) gemv_fp8_kernel(GemvArgs p) {
       }
   }
 
+  if (p.ar_on) {   // row-parallel GEMV -> all-reduce: push this tile into slot [rank] of every peer
+    const unsigned long long epoch = ar_epoch(p.ar);
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int row = row0 + g + ((i & 2) ? 8 : 0);
+        const int tok = tok0 + nt * 8 + 2 * t + (i & 1);
+        if (row >= p.N || tok >= p.T) continue;
+        const size_t off = (size_t)tok * p.N + row;
+        for (int q = 0; q < p.ar.world; q++) ar_slot(p.ar, q, epoch, p.ar.rank)[off] = acc[nt][i];
+      }
+    ar_producer_arrive(p.ar, epoch, /*warp_only=*/true);
+    return;
+  }
   char* outb = reinterpret_cast<char*>(p.out);
   const size_t esz = p.out_f32 ? 4 : 2;
 #pragma unroll
@@ -136,7 +154,7 @@ using namespace moet;
 // a: [B?, T, K] u8 (row stride in bytes = a.stride(-2)); sa: [B?, T, K/64];
 // w: [B?, N, K] u8; sw: [B?, ceil(N/128), ceil(K/128)]; out: [B?, T, N] bf16|f32.
 void gemv_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tensor sw, torch::Tensor out,
-              c10::optional<torch::Tensor> resid) {
+              c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> ar) {
   const bool batched = w.dim() == 3;
   const int B = batched ? w.size(0) : 1;
   const int N = w.size(-2), K = w.size(-1);
@@ -162,6 +180,12 @@ void gemv_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tensor 
   p.out_row_stride = out.stride(-2); p.out_batch_stride = batched ? out.stride(0) : 0;
   p.sw_cols = sw.size(-1);
   p.out_f32 = out.scalar_type() == at::kFloat;
+  p.ar_on = ar.has_value() && ar->defined();
+  if (p.ar_on) {
+    p.ar = ar_desc_from(*ar);
+    TORCH_CHECK(!batched && !p.resid && (int64_t)T * N <= p.ar.cap, "gemv_fp8: all-reduce push needs an unbatched GEMV, "
+                "no residual and T*N <= the slot capacity");
+  }
   TORCH_CHECK(p.out_f32 || out.scalar_type() == at::kBFloat16, "gemv_fp8: out must be bf16 or f32");
   const int nchunks = K / 64;
   auto stream = at::cuda::getCurrentCUDAStream();

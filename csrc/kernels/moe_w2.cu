@@ -20,6 +20,7 @@
 //   with FMAs, exactly as the format defines the dequantised weight.
 // * Misses (slot < 0) write zero rows and bump a miss counter.
 #include "common.cuh"
+#include "symm.cuh"
 #include "torch_glue.h"
 
 namespace moet {
@@ -146,8 +147,10 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int* __res
                                    const float* __restrict__ wts, int k, int H,
                                    const __nv_bfloat16* __restrict__ resid,
                                    const __nv_bfloat16* __restrict__ shared_out,
-                                   __nv_bfloat16* __restrict__ out, float* __restrict__ out_f32) {
+                                   __nv_bfloat16* __restrict__ out, float* __restrict__ out_f32,
+                                   int ar_on, ArDesc ar) {
   const int tok = blockIdx.x;
+  const unsigned long long epoch = ar_on ? ar_epoch(ar) : 0ull;
   __shared__ int pos[32];
   __shared__ float w[32];
   if (threadIdx.x < k) {
@@ -159,11 +162,24 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int* __res
   for (int h = h_begin + threadIdx.x * 4; h < h_end; h += blockDim.x * 4) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int j = 0; j < k; j++) {
+      if (pos[j] < 0) continue;   // routed to an expert another rank owns
       const float4 v = *reinterpret_cast<const float4*>(y + (size_t)pos[j] * H + h);
       acc.x = fmaf(w[j], v.x, acc.x); acc.y = fmaf(w[j], v.y, acc.y);
       acc.z = fmaf(w[j], v.z, acc.z); acc.w = fmaf(w[j], v.w, acc.w);
     }
     float r[4] = {acc.x, acc.y, acc.z, acc.w};
+    if (ar_on) {   // expert combine -> all-reduce: push the partial (experts + shared) to every peer
+      float4 v4 = acc;
+      if (shared_out) {
+        v4.x += __bfloat162float(shared_out[(size_t)tok * H + h]);
+        v4.y += __bfloat162float(shared_out[(size_t)tok * H + h + 1]);
+        v4.z += __bfloat162float(shared_out[(size_t)tok * H + h + 2]);
+        v4.w += __bfloat162float(shared_out[(size_t)tok * H + h + 3]);
+      }
+      for (int q = 0; q < ar.world; q++)
+        *reinterpret_cast<float4*>(ar_slot(ar, q, epoch, ar.rank) + (size_t)tok * H + h) = v4;
+      continue;
+    }
 #pragma unroll
     for (int i = 0; i < 4; i++) {
       if (shared_out) r[i] += __bfloat162float(shared_out[(size_t)tok * H + h + i]);
@@ -172,6 +188,7 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int* __res
       if (out_f32) out_f32[(size_t)tok * H + h + i] = r[i];
     }
   }
+  if (ar_on) ar_producer_arrive(ar, epoch);
 }
 
 }  // namespace moet
@@ -215,13 +232,20 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
 
 void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::optional<torch::Tensor> resid,
                  c10::optional<torch::Tensor> shared_out, c10::optional<torch::Tensor> out,
-                 c10::optional<torch::Tensor> out_f32) {
+                 c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> ar) {
   const int T = wts.size(0), k = wts.size(1), H = y.size(1);
+  const int ar_on = ar.has_value() && ar->defined();
+  ArDesc d{};
+  if (ar_on) {
+    d = ar_desc_from(*ar);
+    TORCH_CHECK(!resid.has_value() || !resid->defined(), "moe_combine: the all-reduce push takes no residual");
+    TORCH_CHECK((int64_t)T * H <= d.cap, "moe_combine: T*H exceeds the all-reduce slot");
+  }
   TORCH_CHECK(H % 4 == 0 && k <= 32, "moe_combine: H % 4, k <= 32");
   if (T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   moe_combine_kernel<<<dim3(T, (H + 1023) / 1024), 256, 0, stream>>>(y.data_ptr<float>(), pos_of.data_ptr<int>(), wts.data_ptr<float>(), k, H,
                                             (const __nv_bfloat16*)opt_ptr(resid), (const __nv_bfloat16*)opt_ptr(shared_out),
-                                            (__nv_bfloat16*)opt_ptr(out), (float*)opt_ptr(out_f32));
+                                            (__nv_bfloat16*)opt_ptr(out), (float*)opt_ptr(out_f32), ar_on, d);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

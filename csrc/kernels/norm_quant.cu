@@ -11,6 +11,7 @@
 // (P:4388-4401); here it is fused into the producer and the group is 64 so
 // it also matches every K-shard of the experts under TP.
 #include "common.cuh"
+#include "symm.cuh"
 #include "torch_glue.h"
 
 namespace moet {
@@ -65,13 +66,31 @@ __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x_in,
                                      __nv_bfloat16* __restrict__ y_out,
                                      uint8_t* __restrict__ q0, uint8_t* __restrict__ s0,
                                      uint8_t* __restrict__ q1, uint8_t* __restrict__ s1,
-                                     int in_stride, int ostride) {
+                                     int in_stride, int ostride, int ar_on, ArDesc ar) {
   const int row = blockIdx.x;
   const int k0 = threadIdx.x * VEC;
   float v[VEC];
   const __nv_bfloat16* xr = x_in + (size_t)row * in_stride + k0;
 #pragma unroll
   for (int i = 0; i < VEC; i++) v[i] = __bfloat162float(xr[i]);
+  if (ar_on) {   // all-reduce consumer: x = residual + sum over ranks (rank order) of the pushed partials
+    const unsigned long long epoch = ar_epoch(ar);
+    if (ar_consumer_wait(ar, epoch)) {
+      float s[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; i++) s[i] = 0.f;
+      for (int r = 0; r < ar.world; r++) {
+        const float* src = ar_slot(ar, ar.rank, epoch, r) + (size_t)row * H + k0;
+#pragma unroll
+        for (int i = 0; i < VEC; i += 4) {
+          const float4 f = *reinterpret_cast<const float4*>(src + i);
+          s[i] += f.x; s[i + 1] += f.y; s[i + 2] += f.z; s[i + 3] += f.w;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < VEC; i++) v[i] += s[i];
+    }
+  }
   if (add) {
     const __nv_bfloat16* ar = add + (size_t)row * H + k0;
 #pragma unroll
@@ -110,6 +129,7 @@ __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x_in,
   }
   if (q0) quant_store<VEC>(v, row, k0, H, 0, q0, s0, ostride);
   if (q1) quant_store<VEC>(v, row, k0, H, 1, q1, s1, ostride);
+  if (ar_on) ar_consumer_done(ar);
 }
 
 // SwiGLU: in [rows, 2I] f32 (gate | up), out e4m3 [rows, I].
@@ -158,7 +178,8 @@ using namespace moet;
 void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> add, c10::optional<torch::Tensor> x_out,
                    torch::Tensor w, double eps, c10::optional<torch::Tensor> y_out,
                    c10::optional<torch::Tensor> q0, c10::optional<torch::Tensor> s0,
-                   c10::optional<torch::Tensor> q1, c10::optional<torch::Tensor> s1, int64_t ostride) {
+                   c10::optional<torch::Tensor> q1, c10::optional<torch::Tensor> s1, int64_t ostride,
+                   c10::optional<torch::Tensor> ar) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16, "x must be cuda bf16");
   const int rows = x.size(0), H = w.size(0);
   TORCH_CHECK(x.stride(1) == 1, "x inner stride must be 1");
@@ -170,11 +191,19 @@ void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> add, c10::optio
   TORCH_CHECK(H >= 128, "rmsnorm_quant: H must be >= 128");
   const int threads = H / vec;
   auto kern = vec == 16 ? rmsnorm_quant_kernel<16> : (vec == 8 ? rmsnorm_quant_kernel<8> : rmsnorm_quant_kernel<4>);
+  const int ar_on = ar.has_value() && ar->defined();
+  ArDesc d{};
+  if (ar_on) {
+    d = ar_desc_from(*ar);
+    TORCH_CHECK(x_out.has_value() && x_out->defined() && !(add.has_value() && add->defined()),
+                "rmsnorm_quant: the all-reduce consumer writes x_out = x + sum of partials (no add)");
+    TORCH_CHECK((int64_t)rows * H <= d.cap, "rmsnorm_quant: rows*H exceeds the all-reduce slot");
+  }
   kern<<<rows, threads, 0, stream>>>(
       (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)opt_ptr(add),
       (__nv_bfloat16*)opt_ptr(x_out), (const __nv_bfloat16*)w.data_ptr(), (float)eps, H,
       (__nv_bfloat16*)opt_ptr(y_out), (uint8_t*)opt_ptr(q0), (uint8_t*)opt_ptr(s0),
-      (uint8_t*)opt_ptr(q1), (uint8_t*)opt_ptr(s1), (int)x.stride(0), (int)(ostride ? ostride : H));
+      (uint8_t*)opt_ptr(q1), (uint8_t*)opt_ptr(s1), (int)x.stride(0), (int)(ostride ? ostride : H), ar_on, d);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

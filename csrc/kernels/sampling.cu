@@ -98,7 +98,8 @@ __global__ void mtp_finalize_kernel(const int* __restrict__ targets, const int* 
 template <typename T>
 __global__ void argmax_split_kernel(const T* __restrict__ logits, long long stride, int V, int want_lse,
                                     float* __restrict__ part, int* __restrict__ counter, int* __restrict__ ids,
-                                    float* __restrict__ lse, int* __restrict__ status) {
+                                    float* __restrict__ lse, int* __restrict__ status,
+                                    float2* __restrict__ mv = nullptr, int id_offset = 0) {
   const int row = blockIdx.x, S = gridDim.y, sp = blockIdx.y;
   const int per = (V + S - 1) / S, lo = sp * per, hi = min(V, lo + per);
   const T* x = logits + (size_t)row * stride;
@@ -154,16 +155,32 @@ __global__ void argmax_split_kernel(const T* __restrict__ logits, long long stri
     lse[row] = M + __logf(tot);
   }
   if (I < 0 || I >= V) { I = 0; set_status(status, kBadValue); }
-  ids[row] = I;
+  if (ids) ids[row] = I + id_offset;
+  if (mv) mv[row] = make_float2(M, __int_as_float(I + id_offset));
   counter[row] = 0;
+}
+
+// Vocab-parallel argmax merge: parts [W, R] of (max, id bits) from W ranks (ids
+// already global) -> ids[R]; ties go to the smaller id, as in the 1-rank argmax.
+__global__ void argmax_merge_kernel(const float2* __restrict__ parts, int W, int R, int* __restrict__ ids) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= R) return;
+  float M = -INFINITY; int I = 0x7fffffff;
+  for (int w = 0; w < W; w++) {
+    const float2 p = parts[(size_t)w * R + r];
+    const int id = __float_as_int(p.y);
+    if (p.x > M || (p.x == M && id < I)) { M = p.x; I = id; }
+  }
+  ids[r] = I == 0x7fffffff ? 0 : I;
 }
 
 }  // namespace moet
 
 using namespace moet;
 
-void argmax_split(torch::Tensor logits, torch::Tensor ids, c10::optional<torch::Tensor> lse,
-                  c10::optional<torch::Tensor> status, torch::Tensor part, torch::Tensor counter) {
+void argmax_split(torch::Tensor logits, c10::optional<torch::Tensor> ids, c10::optional<torch::Tensor> lse,
+                  c10::optional<torch::Tensor> status, torch::Tensor part, torch::Tensor counter,
+                  c10::optional<torch::Tensor> mv, int64_t id_offset) {
   const int R = logits.size(0), V = logits.size(1);
   TORCH_CHECK(logits.stride(1) == 1, "argmax_split: inner stride 1");
   const int S = part.size(1);
@@ -174,11 +191,23 @@ void argmax_split(torch::Tensor logits, torch::Tensor ids, c10::optional<torch::
   const int want = lse.has_value() && lse->defined();
   if (logits.scalar_type() == at::kFloat)
     argmax_split_kernel<float><<<grid, 256, 0, stream>>>(logits.data_ptr<float>(), logits.stride(0), V, want,
-        part.data_ptr<float>(), counter.data_ptr<int>(), ids.data_ptr<int>(), (float*)opt_ptr(lse), (int*)opt_ptr(status));
+        part.data_ptr<float>(), counter.data_ptr<int>(), (int*)opt_ptr(ids), (float*)opt_ptr(lse), (int*)opt_ptr(status),
+        (float2*)opt_ptr(mv), (int)id_offset);
   else
     argmax_split_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>((const __nv_bfloat16*)logits.data_ptr(),
-        logits.stride(0), V, want, part.data_ptr<float>(), counter.data_ptr<int>(), ids.data_ptr<int>(),
-        (float*)opt_ptr(lse), (int*)opt_ptr(status));
+        logits.stride(0), V, want, part.data_ptr<float>(), counter.data_ptr<int>(), (int*)opt_ptr(ids),
+        (float*)opt_ptr(lse), (int*)opt_ptr(status), (float2*)opt_ptr(mv), (int)id_offset);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void argmax_merge(torch::Tensor parts, torch::Tensor ids) {
+  TORCH_CHECK(parts.scalar_type() == at::kFloat && parts.dim() == 3 && parts.size(2) == 2 && parts.is_contiguous(),
+              "argmax_merge: parts [W, R, 2] f32");
+  const int W = parts.size(0), R = parts.size(1);
+  TORCH_CHECK(ids.numel() >= R, "argmax_merge: ids too small");
+  if (R == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  argmax_merge_kernel<<<(R + 127) / 128, 128, 0, stream>>>((const float2*)parts.data_ptr(), W, R, ids.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

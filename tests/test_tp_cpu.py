@@ -1,0 +1,35 @@
+"""Tensor-parallel sharding on CPU ranks (gloo): a TP=2 oracle forward over
+sharded weights (heads, FFN shards, expert intermediate shards, vocab-parallel
+head) computes the same logits as the unsharded model."""
+import torch
+
+from mp_util import run_ranks
+from vllm_moet_b200.config import tiny_config
+from vllm_moet_b200.models import reference as ref
+from vllm_moet_b200.models.weights import random_weights
+
+
+def _tp_forward(rank, world):
+    import torch.distributed as dist
+    cfg = tiny_config()
+    toks = torch.tensor([5, 17, 300, 42, 7, 99, 3, 250])
+    pos = torch.arange(len(toks))
+    cs = ref.rope_cos_sin(cfg, 64)
+    full = random_weights(cfg, "cpu", seed=3)
+    want, _ = ref.forward(full, toks, pos, cs)
+    mw = random_weights(cfg, "cpu", seed=3, tp_rank=rank, tp_size=world)
+    with ref.tp_context(dist.group.WORLD):
+        got, hid = ref.forward(mw, toks, pos, cs)
+        nxt = torch.cat([toks[1:], got[-1:].argmax(-1)])
+        mtp_got, _ = ref.mtp_forward(mw, hid, nxt, pos, cs)
+    mtp_want, _ = ref.mtp_forward(full, ref.forward(full, toks, pos, cs)[1], nxt, pos, cs)
+    return (float((got - want).abs().max()), float(want.abs().max()),
+            float((mtp_got - mtp_want).abs().max()), mw.lm_head.shape[0], cfg.vocab)
+
+
+def test_tp2_forward_matches_single_rank():
+    res = run_ranks(_tp_forward, 2)
+    for err, scale, mtp_err, v_local, vocab in res:
+        assert v_local * 2 == vocab
+        assert err <= 1e-4 * max(scale, 1.0), (err, scale)
+        assert mtp_err <= 1e-4 * max(scale, 1.0), mtp_err

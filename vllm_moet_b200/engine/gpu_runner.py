@@ -102,6 +102,10 @@ class NativeRunner:
         self.scale = 1.0 / math.sqrt(cfg.qk_head_dim)
         self.graphs = {}
         self.tp_group = None
+        self.tp_rank, self.tp_size = mw.tp_rank, mw.tp_size
+        self.ar = None            # fused peer-memory all-reduce (SymmAllReduce) for decode-sized steps
+        self._pend = None         # (residual, out) of a pushed reduction the next RMSNorm completes
+        self._fused = False
         self.nsplit = 8
         import os
         self.debug_finite = os.environ.get("MOET_DEBUG_FINITE", "0") == "1"
@@ -150,7 +154,15 @@ class NativeRunner:
         part = self.ws.get("argmax.part", (max(R, 1), 32, 3), torch.float32)
         assert R <= 8192, "argmax rows"
         cnt = self.ws.zeros("argmax.cnt", (8192,), torch.int32)
-        self.C.argmax_split(logits, ids, None, self.status, part, cnt)
+        if self.tp_group is None:
+            self.C.argmax_split(logits, ids, None, self.status, part, cnt)
+            return
+        # vocab-parallel head: local (max, global id) per row, gathered, merged
+        mv = self.ws.get("argmax.mv", (R, 2), torch.float32)
+        self.C.argmax_split(logits, None, None, self.status, part, cnt, mv, self.tp_rank * logits.shape[1])
+        allmv = self.ws.get("argmax.all", (self.tp_size, R, 2), torch.float32)
+        torch.distributed.all_gather_into_tensor(allmv, mv, group=self.tp_group)
+        self.C.argmax_merge(allmv, ids)
 
     def _router_w(self, lw):
         w = getattr(lw, "_router_w_bf16", None)
@@ -159,16 +171,53 @@ class NativeRunner:
             lw._router_w_bf16 = w
         return w
 
+    def set_tp_group(self, group, fused: Optional[bool] = None):
+        """Join a tensor-parallel group.  Decode-sized reductions then run fused
+        over peer memory (producer epilogues push, the next RMSNorm reduces);
+        prefill-sized ones use NCCL all-reduce.  MOET_TP_FUSED=0 selects NCCL
+        everywhere (the baseline)."""
+        import os
+        self.tp_group = group
+        if fused is None:
+            fused = os.environ.get("MOET_TP_FUSED", "1") != "0"
+        if fused and group is not None:
+            from ..parallel.symm import SymmAllReduce
+            self.ar = SymmAllReduce(group, 128 * self.cfg.hidden, self.dev, self.status)
+
     def _tp_allreduce(self, t):
         if self.tp_group is not None:
             torch.distributed.all_reduce(t, group=self.tp_group)
+
+    def _norm_in(self, x, w, y_out=None, q0=None, s0=None, q1=None, s1=None, ostride=0):
+        """RMSNorm + quant of a sublayer input; completes a pending fused
+        all-reduce first (x = residual + sum of the ranks' partials, written to x)."""
+        pend, self._pend = self._pend, None
+        if pend is not None:
+            resid, xout = pend
+            assert xout.data_ptr() == x.data_ptr()
+            self.C.rmsnorm_quant(resid, None, xout, w, self.cfg.rms_eps, y_out, q0, s0, q1, s1, ostride, self.ar.desc)
+        else:
+            self.C.rmsnorm_quant(x, None, None, w, self.cfg.rms_eps, y_out, q0, s0, q1, s1, ostride)
+
+    def _row_parallel_out(self, aq, as_, lin, x, out, T):
+        """out = x + all-reduce(aq @ lin^T) for a row-parallel linear."""
+        if self.tp_group is None:
+            self._gemv(aq, as_, lin, out, x)
+        elif self._fused:
+            self.C.gemv_fp8(aq, as_, lin.w, lin.s, out, None, self.ar.desc)
+            self._pend = (x, out)
+        else:
+            part = self.ws.get("rp_part", (T, self.cfg.hidden), torch.bfloat16)
+            self._gemv(aq, as_, lin, part)
+            self._tp_allreduce(part)
+            torch.add(x, part, out=out)
 
     # ------------------------------------------------------------------ layer
     def _attention(self, lw: LayerWeights, x, ctx: StepCtx, cache, li, out):
         cfg, C, T, Hh = self.cfg, self.C, ctx.T, self.Hh
         H, ql, lat, rope, nope, vd = cfg.hidden, cfg.q_lora_rank, cfg.kv_lora_rank, cfg.qk_rope_dim, cfg.qk_nope_dim, cfg.v_head_dim
         hq, hs = self._fp8("h", T, H)
-        C.rmsnorm_quant(x, None, None, lw.attn_norm, cfg.rms_eps, None, hq, hs, None, None, 0)
+        self._norm_in(x, lw.attn_norm, None, hq, hs)
         qkva = self.ws.get("qkva", (T, ql + lat + rope), torch.bfloat16)
         self._gemv(hq, hs, lw.qkv_a, qkva)
         qaq, qas = self._fp8("qa", T, ql)
@@ -207,13 +256,7 @@ class NativeRunner:
             C.q_prep(qb, Hh, nope, rope, ctx.pos, self.cos_sin, None, None, None, 0, qf)
             C.mla_prefill(qf, kvb.view(T, Hh, nope + vd), kr, ctx.cu_seqlens, ctx.max_len, self.scale,
                           ovq, ovs, None)
-        if self.tp_group is None:
-            self._gemv(ovq, ovs, lw.o, out, x)
-        else:
-            part = self.ws.get("attn_part", (T, H), torch.bfloat16)
-            self._gemv(ovq, ovs, lw.o, part)
-            self._tp_allreduce(part)
-            torch.add(x, part, out=out)
+        self._row_parallel_out(ovq, ovs, lw.o, x, out, T)
 
     def _ffn(self, lw: LayerWeights, x, ctx: StepCtx, out):
         cfg, C, T = self.cfg, self.C, ctx.T
@@ -221,16 +264,16 @@ class NativeRunner:
         hb = self.ws.get("hb", (T, H), torch.bfloat16)
         hq, hs = self._fp8("h", T, H)
         if not lw.is_moe:
-            C.rmsnorm_quant(x, None, None, lw.ffn_norm, cfg.rms_eps, None, hq, hs, None, None, 0)
+            self._norm_in(x, lw.ffn_norm, None, hq, hs)
             I2 = lw.gate_up.w.shape[0]
             gu = self.ws.get("gu", (T, I2), torch.float32)
             self._gemv(hq, hs, lw.gate_up, gu)
             aq, as_ = self._fp8("act", T, I2 // 2)
             C.swiglu_quant(gu, 0.0, None, 0, aq, as_)
-            self._ffn_out(lw.down, aq, as_, x, out, T)
+            self._row_parallel_out(aq, as_, lw.down, x, out, T)
             return
         h2q, h2s = self._fp8("h2", T, H)
-        C.rmsnorm_quant(x, None, None, lw.ffn_norm, cfg.rms_eps, hb, hq, hs, h2q, h2s, 0)
+        self._norm_in(x, lw.ffn_norm, hb, hq, hs, h2q, h2s)
         E, k = cfg.num_experts, cfg.top_k
         logits = self.ws.get("rlogits", (T, E), torch.float32)
         if T <= 64:
@@ -260,6 +303,9 @@ class NativeRunner:
             self._gemv(sq, ss, lw.shared_down, sh)
         if self.tp_group is None:
             C.moe_combine(y2, posof, wts, x, sh, out, None)
+        elif self._fused:
+            C.moe_combine(y2, posof, wts, None, sh, None, None, self.ar.desc)
+            self._pend = (x, out)
         else:
             part = self.ws.get("moe_part", (T, H), torch.bfloat16)
             C.moe_combine(y2, posof, wts, None, sh, part, None)
@@ -320,18 +366,9 @@ class NativeRunner:
                       H, I, MB, self.miss)
         return y2, posof
 
-    def _ffn_out(self, lin, aq, as_, x, out, T):
-        if self.tp_group is None:
-            self._gemv(aq, as_, lin, out, x)
-        else:
-            part = self.ws.get("ffn_part", (T, self.cfg.hidden), torch.bfloat16)
-            self._gemv(aq, as_, lin, part)
-            self._tp_allreduce(part)
-            torch.add(x, part, out=out)
-
     def _check(self, name, t):
         """Debug aid (MOET_DEBUG_FINITE=1, eager only): raise at the first non-finite stage output."""
-        if self.debug_finite and not torch.cuda.is_current_stream_capturing():
+        if self.debug_finite and self._pend is None and not torch.cuda.is_current_stream_capturing():
             bad = ~torch.isfinite(t.float())
             if bool(bad.any()):
                 rows = bad.view(t.shape[0], -1).any(-1).nonzero().flatten()[:8].tolist()
@@ -339,6 +376,7 @@ class NativeRunner:
 
     def _layer(self, lw, x, ctx, cache, li):
         H = self.cfg.hidden
+        self._fused = self.ar is not None and ctx.mode == "decode" and self.ar.fits(ctx.T, H)
         x2 = self.ws.get("x_mid", (ctx.T, H), torch.bfloat16)
         self._attention(lw, x, ctx, cache, li, x2)
         self._check(f"attention[{li}] ({ctx.mode})", x2)
@@ -363,9 +401,8 @@ class NativeRunner:
         T = x.shape[0]
         hid = self.ws.get(tag + ".hid", (T, cfg.hidden), torch.bfloat16)
         fq, fs = self._fp8(tag + ".f", T, cfg.hidden)
-        C.rmsnorm_quant(x, None, None, self.mw.final_norm if tag == "main" else self.mw.mtp.head_norm,
-                        cfg.rms_eps, hid, fq, fs, None, None, 0)
-        logits = self.ws.get(tag + ".logits", (T, cfg.vocab), torch.float32)
+        self._norm_in(x, self.mw.final_norm if tag == "main" else self.mw.mtp.head_norm, hid, fq, fs)
+        logits = self.ws.get(tag + ".logits", (T, self.mw.lm_head.w.shape[0]), torch.float32)
         self._gemv(fq, fs, self.mw.lm_head, logits)
         self._check(f"lm_head ({tag})", logits)
         return hid, logits

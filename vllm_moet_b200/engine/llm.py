@@ -74,7 +74,7 @@ class LLM:
             self.blocks = BlockManager(nb)
             self.runner = NativeRunner(self.mw, self.ecfg, nb, self.device)
             if tp_group is not None:
-                self.runner.tp_group = tp_group
+                self.runner.set_tp_group(tp_group)
             self._DecodeState = DecodeState
             self._states = {}
             self._pin_active = None

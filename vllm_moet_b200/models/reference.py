@@ -27,6 +27,45 @@ from ..config import ModelConfig
 from .weights import LayerWeights, ModelWeights
 
 
+_TP_GROUP = None
+
+
+class tp_context:
+    """Run the oracle as one rank of a tensor-parallel group (weights from
+    ``random_weights(..., tp_rank, tp_size)``): partial outputs of the o and
+    down projections are all-reduced and vocab-sharded logits all-gathered."""
+
+    def __init__(self, group):
+        self.group = group
+
+    def __enter__(self):
+        global _TP_GROUP
+        self.prev, _TP_GROUP = _TP_GROUP, self.group
+        return self
+
+    def __exit__(self, *a):
+        global _TP_GROUP
+        _TP_GROUP = self.prev
+
+
+def _allreduce(x: torch.Tensor) -> torch.Tensor:
+    if _TP_GROUP is not None:
+        import torch.distributed as dist
+        x = x.contiguous()
+        dist.all_reduce(x, group=_TP_GROUP)
+    return x
+
+
+def _gather_vocab(logits: torch.Tensor) -> torch.Tensor:
+    if _TP_GROUP is None:
+        return logits
+    import torch.distributed as dist
+    n = dist.get_world_size(_TP_GROUP)
+    parts = [torch.empty_like(logits) for _ in range(n)]
+    dist.all_gather(parts, logits.contiguous(), group=_TP_GROUP)
+    return torch.cat(parts, dim=-1)
+
+
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     x = x.float()
     return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w.float()
@@ -121,7 +160,7 @@ class RefKV:
 def attention(cfg: ModelConfig, lw: LayerWeights, x: torch.Tensor, positions: torch.Tensor, cs: torch.Tensor,
               cache: Optional[RefKV] = None, li: int = 0, heads: Optional[int] = None) -> torch.Tensor:
     """x [T, H] (normed), positions [T] (contiguous, appended after the cache) -> [T, H]."""
-    Hh = heads or cfg.num_heads
+    Hh = heads or lw.q_b.shape[0] // cfg.qk_head_dim
     T = x.shape[0]
     nope, rope, vd, lat = cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim, cfg.kv_lora_rank
     qkva = x.float() @ lw.qkv_a.dequant().t()
@@ -153,9 +192,9 @@ def attention(cfg: ModelConfig, lw: LayerWeights, x: torch.Tensor, positions: to
 
 def decoder_layer(cfg, lw, x, positions, cs, cache=None, li=0):
     h = rms_norm(x, lw.attn_norm, cfg.rms_eps)
-    x = x + attention(cfg, lw, h, positions, cs, cache, li)
+    x = x + _allreduce(attention(cfg, lw, h, positions, cs, cache, li))
     h = rms_norm(x, lw.ffn_norm, cfg.rms_eps)
-    return x + (moe_block(cfg, lw, h) if lw.is_moe else dense_ffn(cfg, lw, h))
+    return x + _allreduce(moe_block(cfg, lw, h) if lw.is_moe else dense_ffn(cfg, lw, h))
 
 
 def forward(mw: ModelWeights, tokens: torch.Tensor, positions: torch.Tensor, cs: torch.Tensor,
@@ -166,7 +205,7 @@ def forward(mw: ModelWeights, tokens: torch.Tensor, positions: torch.Tensor, cs:
     for li, lw in enumerate(mw.layers):
         x = decoder_layer(cfg, lw, x, positions, cs, cache, li)
     h = rms_norm(x, mw.final_norm, cfg.rms_eps)
-    return h @ mw.lm_head.dequant().t(), h
+    return _gather_vocab(h @ mw.lm_head.dequant().t()), h
 
 
 def mtp_forward(mw: ModelWeights, hidden: torch.Tensor, next_tokens: torch.Tensor, positions: torch.Tensor,
@@ -178,7 +217,7 @@ def mtp_forward(mw: ModelWeights, hidden: torch.Tensor, next_tokens: torch.Tenso
     x = torch.cat([e, hn], dim=-1) @ m.eh_proj.dequant().t()
     x = decoder_layer(cfg, m.layer, x, positions, cs, cache, 0)
     h = rms_norm(x, m.head_norm, cfg.rms_eps)
-    return h @ mw.lm_head.dequant().t(), h
+    return _gather_vocab(h @ mw.lm_head.dequant().t()), h
 
 
 def greedy_generate(mw: ModelWeights, prompt: list, max_tokens: int) -> list:

@@ -261,44 +261,99 @@ def quantize_experts_cpu(w13: torch.Tensor, w2: torch.Tensor, layout: ExpertLayo
             out_pool[e, off_s:off_s + N * K // 32] = planes.pack_scales(sc).to(out_pool.device)
 
 
+def _pad_to(n: int, m: int) -> int:
+    return -(-n // m) * m
+
+
+def tp_ffn_shard(I: int, tp_size: int, dtype: str) -> int:
+    """Per-rank intermediate size of a TP-sharded dense FFN: I/tp rounded up to the
+    128-row FP8 block (zero rows/columns pad the shard; silu(0) * 0 adds nothing)."""
+    per = -(-I // tp_size)
+    return _pad_to(per, 128) if dtype == "fp8" else per
+
+
+def _shard_ffn(gu: torch.Tensor, down: torch.Tensor, I: int, tp_rank: int, tp_size: int, Ip: int):
+    """Column-parallel gate/up [2I, H] and row-parallel down [H, I] -> this rank's
+    [2Ip, H] and [H, Ip] (gate rows first, then up rows)."""
+    if tp_size == 1 and Ip == I:
+        return gu, down
+    per = -(-I // tp_size)
+    lo, hi = tp_rank * per, min(I, (tp_rank + 1) * per)
+    n = max(0, hi - lo)
+    H = gu.shape[1]
+    g = gu.new_zeros((2 * Ip, H))
+    d = down.new_zeros((down.shape[0], Ip))
+    g[:n] = gu[lo:hi]
+    g[Ip:Ip + n] = gu[I + lo:I + hi]
+    d[:, :n] = down[:, lo:hi]
+    return g, d
+
+
 def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0, tp_size=1,
                 expert_chunk: int = 16) -> LayerWeights:
+    """One decoder layer, sharded for rank `tp_rank` of a `tp_size` tensor-parallel
+    group.  Full matrices are drawn first (the same draws for every TP size) and
+    then sliced, so TP runs compute the same function as one GPU:
+      * MLA: q_b / kv_b rows and o columns split by head (q_a / kv_a replicated);
+      * dense FFN and shared expert: gate/up rows and down columns split, each
+        shard zero-padded to the FP8 block;
+      * routed experts: every expert's intermediate dimension split (w13 rows,
+        w2 columns), so each rank streams 1/tp of every routed expert."""
     H, dt = cfg.hidden, cfg.dense_dtype
-    Hh = cfg.num_heads // tp_size
+    nh = cfg.num_heads
+    assert nh % tp_size == 0, "num_heads must divide by the TP size"
+    Hh = nh // tp_size
     qk = cfg.qk_head_dim
-    lin = lambda shape: make_linear(rng.normal(shape), dt)  # noqa: E731
+    nope_v = cfg.qk_nope_dim + cfg.v_head_dim
+    lin = lambda w: make_linear(w, dt)  # noqa: E731
     ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=dev)  # noqa: E731
     q_lora = cfg.q_lora_rank
+    h0, h1 = tp_rank * Hh, (tp_rank + 1) * Hh
+    q_b = rng.normal((nh * qk, q_lora))[h0 * qk:h1 * qk]
+    kv_b = rng.normal((nh * nope_v, cfg.kv_lora_rank))[h0 * nope_v:h1 * nope_v]
+    o = rng.normal((H, nh * cfg.v_head_dim))[:, h0 * cfg.v_head_dim:h1 * cfg.v_head_dim]
     lw = LayerWeights(
         attn_norm=ones(H),
-        qkv_a=lin((q_lora + cfg.kv_lora_rank + cfg.qk_rope_dim, H)),
+        qkv_a=lin(rng.normal((q_lora + cfg.kv_lora_rank + cfg.qk_rope_dim, H))),
         q_a_norm=ones(q_lora),
         kv_a_norm=ones(cfg.kv_lora_rank),
-        q_b=lin((Hh * qk, q_lora)),
-        kv_b=lin((Hh * (cfg.qk_nope_dim + cfg.v_head_dim), cfg.kv_lora_rank)),
-        o=lin((H, Hh * cfg.v_head_dim)),
+        q_b=lin(q_b.contiguous()),
+        kv_b=lin(kv_b.contiguous()),
+        o=lin(o.contiguous()),
         ffn_norm=ones(H),
     )
     if isinstance(lw.kv_b, Fp8Linear):
         lw.w_uk_t, lw.w_uv = _derive_absorb(lw.kv_b, cfg, Hh)
     if not moe:
-        I = cfg.dense_intermediate // tp_size
-        lw.gate_up = lin((2 * I, H))
-        lw.down = lin((H, I))
+        I = cfg.dense_intermediate
+        Ip = tp_ffn_shard(I, tp_size, dt) if tp_size > 1 else I
+        gu, dn = _shard_ffn(rng.normal((2 * I, H)), rng.normal((H, I)), I, tp_rank, tp_size, Ip)
+        lw.gate_up, lw.down = lin(gu.contiguous()), lin(dn.contiguous())
         return lw
-    E, I = cfg.num_experts, cfg.moe_intermediate // tp_size
+    E, Ifull = cfg.num_experts, cfg.moe_intermediate
+    assert Ifull % tp_size == 0 and (Ifull // tp_size) % 64 == 0, "expert intermediate / tp must be a multiple of 64"
+    I = Ifull // tp_size
     lw.router_w = rng.normal((E, H)).to(torch.bfloat16).float()   # bf16-valued gate weights
     lw.router_bias = torch.zeros(E, dtype=torch.float32, device=dev)
-    Is = cfg.moe_intermediate * cfg.num_shared_experts // tp_size
     if cfg.num_shared_experts:
-        lw.shared_gate_up = lin((2 * Is, H))
-        lw.shared_down = lin((H, Is))
+        Is = cfg.moe_intermediate * cfg.num_shared_experts
+        Isp = tp_ffn_shard(Is, tp_size, dt) if tp_size > 1 else Is
+        gu, dn = _shard_ffn(rng.normal((2 * Is, H)), rng.normal((H, Is)), Is, tp_rank, tp_size, Isp)
+        lw.shared_gate_up, lw.shared_down = lin(gu.contiguous()), lin(dn.contiguous())
     layout = ExpertLayout(H=H, I=I)
+    lo = tp_rank * I
+
+    def shard13(w):   # [.., 2*Ifull, H] -> [.., 2I, H]
+        return torch.cat([w[..., lo:lo + I, :], w[..., Ifull + lo:Ifull + lo + I, :]], dim=-2).contiguous()
+
+    def shard2(w):    # [.., H, Ifull] -> [.., H, I]
+        return w[..., lo:lo + I].contiguous()
+
     if cfg.expert_scale == "fp16_amax4":
         # CPU tiny config: fp16 group-32 scale = max|w|/4; keep the dequantized experts
         w13s, w2s = [], []
         for e in range(E):
-            a = rng.normal((2 * I, H)); b = rng.normal((H, I))
+            a = shard13(rng.normal((2 * Ifull, H))); b = shard2(rng.normal((H, Ifull)))
             c, s = codebook.f32_to_codes_fp16_amax4(a); w13s.append(codebook.dequant_codes_fp16(c, s))
             c, s = codebook.f32_to_codes_fp16_amax4(b); w2s.append(codebook.dequant_codes_fp16(c, s))
         pool = torch.zeros(E, 16, dtype=torch.uint8, device=dev)
@@ -308,8 +363,8 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
     pool = torch.empty(E, layout.slot_bytes, dtype=torch.uint8, device=dev)
     for e0 in range(0, E, expert_chunk):
         n = min(expert_chunk, E - e0)
-        w13 = rng.normal((n, 2 * I, H))
-        w2 = rng.normal((n, H, I))
+        w13 = shard13(rng.normal((n, 2 * Ifull, H)))
+        w2 = shard2(rng.normal((n, H, Ifull)))
         if torch.device(dev).type == "cuda":
             quantize_experts_gpu(w13, w2, layout, pool[e0:e0 + n])
         else:
@@ -317,6 +372,16 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
         del w13, w2
     lw.experts = ExpertPool(layout, pool, torch.arange(E, dtype=torch.int32, device=dev))
     return lw
+
+
+def _vocab_shard(w: torch.Tensor, tp_rank: int, tp_size: int) -> torch.Tensor:
+    """Rows [r*V/tp, (r+1)*V/tp) of a [V, H] head (vocab-parallel lm_head)."""
+    if tp_size == 1:
+        return w
+    V = w.shape[0]
+    assert V % tp_size == 0, "vocab must divide by the TP size"
+    per = V // tp_size
+    return w[tp_rank * per:(tp_rank + 1) * per].contiguous()
 
 
 def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int = 0, tp_size: int = 1,
@@ -330,7 +395,7 @@ def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int =
     layers = [_make_layer(cfg, rng, i, dev, cfg.is_moe_layer(i), tp_rank, tp_size) for i in range(L)]
     mw = ModelWeights(cfg=cfg, embed=embed, layers=layers,
                       final_norm=torch.ones(H, dtype=torch.bfloat16, device=dev),
-                      lm_head=make_linear(rng.normal((cfg.vocab, H)), cfg.dense_dtype),
+                      lm_head=make_linear(_vocab_shard(rng.normal((cfg.vocab, H)), tp_rank, tp_size), cfg.dense_dtype),
                       tp_rank=tp_rank, tp_size=tp_size)
     if with_mtp and cfg.num_mtp_layers:
         mw.mtp = MTPWeights(
