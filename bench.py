@@ -97,10 +97,11 @@ def main():
     st.block_table.copy_(bt)
     runner.prefill([prompt(args.prompt_len)], [bt[0].tolist()], [0], st)
     st.set_active(torch.ones(1, dtype=torch.int32, device="cuda"))
-    counter = LaunchCounter(runner.C)
+    runner.decode_body_eager_warm(st)
+    counter = LaunchCounter(runner.C)     # counts the native launches recorded into the graph
     real_C = runner.C
     runner.C = counter
-    graph = runner.capture(st)
+    graph = runner.capture(st, warm=False)
     launches_per_step = counter.count
     runner.C = real_C
     accepted0 = 0

@@ -21,6 +21,13 @@ void build_pairs(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor ra
                  torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
                  torch::Tensor status);
 void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out);
+void moe_route_fused(torch::Tensor x, torch::Tensor w, torch::Tensor logits, c10::optional<torch::Tensor> bias,
+                     int64_t k, bool sigmoid, int64_t n_group, int64_t topk_group, bool norm, double scaling,
+                     torch::Tensor ids, torch::Tensor wts, int64_t MB, torch::Tensor rank_scratch,
+                     torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
+                     torch::Tensor counter, torch::Tensor status);
+void mla_combine_uv(torch::Tensor o_part, torch::Tensor ml_part, torch::Tensor wuv, torch::Tensor swuv,
+                    torch::Tensor q, torch::Tensor qs);
 void argmax_split(torch::Tensor logits, c10::optional<torch::Tensor> ids, c10::optional<torch::Tensor> lse,
                   c10::optional<torch::Tensor> status, torch::Tensor part, torch::Tensor counter,
                   c10::optional<torch::Tensor> mv, int64_t id_offset);
@@ -109,6 +116,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("build_pairs_padded", &build_pairs_padded);
   m.def("gather_rows", &gather_rows);
   m.def("router_logits", &router_logits);
+  m.def("moe_route_fused", &moe_route_fused);
+  m.def("mla_combine_uv", &mla_combine_uv);
   m.def("tc_gemm_test", &tc_gemm_test);
   m.def("tc_moe_w2", &tc_moe_w2);
   m.def("tc_gemm_fp8", &tc_gemm_fp8);

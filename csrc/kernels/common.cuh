@@ -19,6 +19,18 @@ enum Status : int {
   kBadValue = 4,     // a non-finite value where a finite one is required
 };
 
+// Programmatic dependent launch.  Kernels launched with launch_k() may start
+// while the previous kernel on the stream is still running; each such kernel
+// (1) may touch only immutable data (weights) before pdl_wait(), (2) calls
+// pdl_wait() -- which returns once the previous grid has completed and its
+// writes are visible -- before any other global read or any global write, and
+// (3) calls pdl_trigger() right after, letting the next kernel start its own
+// prologue.  Both are no-ops for a kernel launched without the attribute.
+MOET_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+MOET_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+MOET_DEVICE void pdl_entry() { pdl_wait(); pdl_trigger(); }
+MOET_DEVICE void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 MOET_DEVICE void set_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
@@ -97,6 +109,12 @@ MOET_DEVICE float warp_sum(float v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
+MOET_DEVICE float e4m3_to_f32(uint8_t b) {
+  __nv_fp8_e4m3 v;
+  v.__x = b;
+  return static_cast<float>(v);
+}
+
 MOET_DEVICE float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -138,3 +156,31 @@ MOET_DEVICE uint32_t f32x8_to_e2m1x8(const float* f) {
 }
 
 }  // namespace moet
+
+#include <cstdlib>
+#include <utility>
+// Host: launch with the programmatic-stream-serialization attribute (PDL) unless
+// MOET_PDL=0.  Captured into CUDA graphs as programmatic dependency edges.
+inline bool moet_pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("MOET_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = moet_pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}

@@ -40,6 +40,12 @@ __global__ void __launch_bounds__(256) gemv_fp8_kernel(GemvArgs p) {
   const int row0 = blockIdx.x * 16;
   const int tok0 = blockIdx.y * 8 * NT;
   const int b = blockIdx.z;
+  if (blockIdx.y == 0) {   // weights are immutable: pull this CTA's rows toward L2 while the previous kernel runs
+    const int lines = p.K >> 7, nrows = min(16, p.N - row0);
+    const uint8_t* wbase = p.W + (size_t)b * p.w_batch_stride + (size_t)row0 * p.K;
+    for (int i = threadIdx.x; i < nrows * lines; i += blockDim.x) prefetch_l2(wbase + (size_t)i * 128);
+  }
+  pdl_entry();
   const uint8_t* A = p.A + (size_t)b * p.a_batch_stride;
   const uint8_t* sA = p.sA + (size_t)b * p.sa_batch_stride;
   const uint8_t* W = p.W + (size_t)b * p.w_batch_stride;
@@ -198,7 +204,7 @@ void gemv_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tensor 
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(gemv_fp8_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(gemv_fp8_kernel<NT>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    gemv_fp8_kernel<NT><<<grid, nwarps * 32, smem, stream>>>(p);
+    launch_k(gemv_fp8_kernel<NT>, grid, nwarps * 32, smem, stream, p);
   };
   if (T <= 8) launch(std::integral_constant<int, 1>{});
   else if (T <= 16) launch(std::integral_constant<int, 2>{});

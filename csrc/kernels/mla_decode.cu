@@ -67,6 +67,7 @@ struct MlaDecodeArgs {
 
 template <int MT>
 __global__ void __launch_bounds__(256, 1) mla_decode_kernel(MlaDecodeArgs p) {
+  pdl_entry();
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __nv_bfloat16* kvs = reinterpret_cast<__nv_bfloat16*>(smem_raw);                 // 2 blocks
   __nv_bfloat16* qs = kvs + 2 * kBS * kRow;                                         // [16MT][584]
@@ -80,7 +81,7 @@ __global__ void __launch_bounds__(256, 1) mla_decode_kernel(MlaDecodeArgs p) {
   const int seq = p.seq_of_tok[tok];
   const int L = p.pos_of_tok[tok] + 1;
   const int ntiles = (L + kBS - 1) / kBS;
-  const int tps = (ntiles + p.nsplit - 1) / p.nsplit;
+  const int tps = max(2, (ntiles + p.nsplit - 1) / p.nsplit);   // >= 2 tiles: keeps the KV double buffer busy
   const int t_begin = split * tps, t_end = min(ntiles, t_begin + tps);
 
   if (threadIdx.x == 0) { mbar_init(&bars[0], 1); mbar_init(&bars[1], 1); fence_proxy_async(); }
@@ -247,6 +248,7 @@ __global__ void __launch_bounds__(256, 1) mla_decode_kernel(MlaDecodeArgs p) {
 __global__ void mla_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ ml_part,
                                    int S, int TH, __nv_bfloat16* __restrict__ out,
                                    uint8_t* __restrict__ q, uint8_t* __restrict__ qs) {
+  pdl_entry();
   const int row = blockIdx.x;  // (t, h)
   float M = -INFINITY;
   for (int s = 0; s < S; s++) M = fmaxf(M, ml_part[((size_t)s * TH + row) * 2]);
@@ -289,9 +291,132 @@ __global__ void mla_combine_kernel(const float* __restrict__ o_part, const float
   }
 }
 
+// Split merge fused with the absorbed value projection and its quantisation:
+// one CTA per head h merges the S partial states of every token into o_lat
+// (bf16-rounded, kept in shared memory), applies W_uv[h] (128 x 512, e4m3 with
+// UE8M0 128x128 block scales) and writes ov[t, h*128 + j] as e4m3 with UE8M0
+// per-64 scales -- the input of the o projection.
+constexpr int kVD = 128, kTC = 16;   // value head dim, tokens per smem chunk
+__global__ void __launch_bounds__(512) mla_combine_uv_kernel(const float* __restrict__ o_part,
+                                                             const float* __restrict__ ml_part, int S, int T, int Hh,
+                                                             const uint8_t* __restrict__ wuv,
+                                                             const uint8_t* __restrict__ swuv,
+                                                             uint8_t* __restrict__ q, uint8_t* __restrict__ qs) {
+  __shared__ __align__(16) float olat[kTC][kLat];
+  __shared__ float ov[kTC][kVD];
+  __shared__ float wgt[kTC][32];
+  __shared__ int nact[kTC];
+  const int h = blockIdx.x, TH = T * Hh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint8_t* W = wuv + (size_t)h * kVD * kLat;
+  const uint8_t* SW = swuv + (size_t)h * (kLat / 128);
+  // thread (row j, quarter qk) owns W[j][128*qk .. +128) -- one scale block; immutable, so it is
+  // loaded before the dependency wait
+  const int j = threadIdx.x >> 2, qk = threadIdx.x & 3, nwarps = blockDim.x >> 5;
+  uint4 wrow[8];
+#pragma unroll
+  for (int u = 0; u < 8; u++)
+    wrow[u] = __ldg(reinterpret_cast<const uint4*>(W + (size_t)j * kLat + qk * 128) + u);
+  const float wsc = ue8m0_to_float(__ldg(SW + qk));
+  pdl_entry();
+  const int tbeg = blockIdx.y * kTC, tend = min(T, tbeg + kTC);
+  for (int t0 = tbeg; t0 < tend; t0 += kTC) {
+    const int nt = min(kTC, T - t0);
+    // split weights exp2(m_s - M) / sum: one warp per token (S <= 32)
+    for (int tt = warp; tt < nt; tt += nwarps) {
+      const int row = (t0 + tt) * Hh + h;
+      const float m = lane < S ? ml_part[((size_t)lane * TH + row) * 2] : -INFINITY;
+      const float l = lane < S ? ml_part[((size_t)lane * TH + row) * 2 + 1] : 0.f;
+      const float M = warp_max(m);
+      const float e = m == -INFINITY ? 0.f : exp2f(m - M);
+      const float den = warp_sum(e * l);
+      wgt[tt][lane] = den > 0.f ? e / den : 0.f;
+      // active splits form a prefix (each split takes the next range of KV tiles)
+      const unsigned act = __ballot_sync(0xffffffffu, m != -INFINITY);
+      if (lane == 0) nact[tt] = 32 - __clz(act);
+    }
+    __syncthreads();
+    // merge: each thread owns 4 consecutive dims of one token; loads of 4 splits in flight
+    for (int i = threadIdx.x; i < nt * (kLat / 4); i += blockDim.x) {
+      const int tt = i / (kLat / 4), d = (i % (kLat / 4)) * 4;
+      const int row = (t0 + tt) * Hh + h;
+      const int na = nact[tt];
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int sp0 = 0; sp0 < na; sp0 += 4) {
+        float4 pv[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+          pv[u] = sp0 + u < na ? *reinterpret_cast<const float4*>(o_part + ((size_t)(sp0 + u) * TH + row) * kLat + d)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          const float w = sp0 + u < na ? wgt[tt][sp0 + u] : 0.f;
+          v.x = fmaf(w, pv[u].x, v.x); v.y = fmaf(w, pv[u].y, v.y);
+          v.z = fmaf(w, pv[u].z, v.z); v.w = fmaf(w, pv[u].w, v.w);
+        }
+      }
+      float* dst = &olat[tt][d];
+      dst[0] = __bfloat162float(__float2bfloat16(v.x)); dst[1] = __bfloat162float(__float2bfloat16(v.y));
+      dst[2] = __bfloat162float(__float2bfloat16(v.z)); dst[3] = __bfloat162float(__float2bfloat16(v.w));
+    }
+    __syncthreads();
+    // ov[t][j] = sum_k W[j][k] * olat[t][k]: four threads per row, joined by two shuffles
+    for (int tt = 0; tt < nt; tt++) {
+      const float4* op = reinterpret_cast<const float4*>(&olat[tt][qk * 128]);
+      float acc = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const uint8_t* wb = reinterpret_cast<const uint8_t*>(&wrow[u]);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float4 o4 = op[u * 4 + i];
+          acc = fmaf(e4m3_to_f32(wb[4 * i]), o4.x, fmaf(e4m3_to_f32(wb[4 * i + 1]), o4.y,
+                fmaf(e4m3_to_f32(wb[4 * i + 2]), o4.z, fmaf(e4m3_to_f32(wb[4 * i + 3]), o4.w, acc))));
+        }
+      }
+      float v = acc * wsc;
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      if (qk == 0) ov[tt][j] = __bfloat162float(__float2bfloat16(v));
+    }
+    __syncthreads();
+    // quantise: one warp per (token, 64-group), 2 values per lane
+    for (int gi = warp; gi < nt * 2; gi += nwarps) {
+      const int tt = gi >> 1, g0 = (gi & 1) * 64;
+      const float a = ov[tt][g0 + 2 * lane], b = ov[tt][g0 + 2 * lane + 1];
+      const float amax = warp_max(fmaxf(fabsf(a), fabsf(b)));
+      const uint32_t e = ue8m0_for_amax(amax);
+      const float inv = (e >= 1 && e <= 253) ? __uint_as_float((254u - e) << 23) : 0.f;
+      const size_t col = (size_t)h * kVD + g0;
+      uint8_t* dq = q + (size_t)(t0 + tt) * Hh * kVD + col + 2 * lane;
+      dq[0] = f32_to_e4m3(a * inv);
+      dq[1] = f32_to_e4m3(b * inv);
+      if (lane == 0) qs[(size_t)(t0 + tt) * (Hh * kVD / 64) + col / 64] = (uint8_t)e;
+    }
+    __syncthreads();
+  }
+}
+
 }  // namespace moet
 
 using namespace moet;
+
+void mla_combine_uv(torch::Tensor o_part, torch::Tensor ml_part, torch::Tensor wuv, torch::Tensor swuv,
+                    torch::Tensor q, torch::Tensor qs) {
+  const int S = o_part.size(0), T = o_part.size(1), Hh = o_part.size(2);
+  TORCH_CHECK(o_part.size(3) == kLat && S <= 32 && o_part.is_contiguous() && ml_part.is_contiguous(),
+              "mla_combine_uv: o_part [S<=32, T, Hh, 512] contiguous");
+  TORCH_CHECK(wuv.dim() == 3 && wuv.size(0) == Hh && wuv.size(1) == kVD && wuv.size(2) == kLat && wuv.is_contiguous(),
+              "mla_combine_uv: W_uv [Hh, 128, 512]");
+  TORCH_CHECK(swuv.numel() == (int64_t)Hh * (kLat / 128) && swuv.is_contiguous(), "mla_combine_uv: W_uv scales [Hh, 1, 4]");
+  TORCH_CHECK(q.is_contiguous() && q.size(-1) * (q.dim() == 3 ? q.size(1) : 1) == (int64_t)Hh * kVD, "mla_combine_uv: out");
+  if (T == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  launch_k(mla_combine_uv_kernel, dim3(Hh, (T + kTC - 1) / kTC), 512, 0, stream, o_part.data_ptr<float>(), ml_part.data_ptr<float>(), S, T, Hh,
+           (const uint8_t*)wuv.data_ptr(), (const uint8_t*)swuv.data_ptr(), (uint8_t*)q.data_ptr(),
+           (uint8_t*)qs.data_ptr());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 
 void mla_decode(torch::Tensor q, torch::Tensor kv, torch::Tensor block_table, torch::Tensor seq_of_tok,
                 torch::Tensor pos_of_tok, torch::Tensor o_part, torch::Tensor ml_part, double scale,
@@ -318,12 +443,12 @@ void mla_decode(torch::Tensor q, torch::Tensor kv, torch::Tensor block_table, to
     const int MT = 1;
     size_t smem = (size_t)(2 * kBS * kRow + 16 * MT * kRow + 16 * MT * kPRow) * 2 + 8 * 16 * MT * 4 + 16;
     cudaFuncSetAttribute(mla_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    mla_decode_kernel<1><<<grid, 256, smem, stream>>>(p);
+    launch_k(mla_decode_kernel<1>, grid, 256, smem, stream, p);
   } else {
     const int MT = 2;
     size_t smem = (size_t)(2 * kBS * kRow + 16 * MT * kRow + 16 * MT * kPRow) * 2 + 8 * 16 * MT * 4 + 16;
     cudaFuncSetAttribute(mla_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    mla_decode_kernel<2><<<grid, 256, smem, stream>>>(p);
+    launch_k(mla_decode_kernel<2>, grid, 256, smem, stream, p);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -333,7 +458,7 @@ void mla_combine(torch::Tensor o_part, torch::Tensor ml_part, c10::optional<torc
   const int S = o_part.size(0), TH = o_part.size(1) * o_part.size(2);
   if (TH == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  mla_combine_kernel<<<TH, 64, 0, stream>>>(o_part.data_ptr<float>(), ml_part.data_ptr<float>(), S, TH,
+  launch_k(mla_combine_kernel, TH, 64, 0, stream, o_part.data_ptr<float>(), ml_part.data_ptr<float>(), S, TH,
                                             (__nv_bfloat16*)opt_ptr(out), (uint8_t*)opt_ptr(q),
                                             (uint8_t*)opt_ptr(qs));
   C10_CUDA_KERNEL_LAUNCH_CHECK();

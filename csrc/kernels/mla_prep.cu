@@ -19,6 +19,7 @@ __global__ void q_prep_kernel(const __nv_bfloat16* __restrict__ qb, long long qb
                               uint8_t* __restrict__ qn_q, uint8_t* __restrict__ qn_s,
                               __nv_bfloat16* __restrict__ qcat, long long qcat_tok_stride, int qcat_head_stride,
                               int rope_off, __nv_bfloat16* __restrict__ q_out /* optional [T,Hh,nope+rope] */) {
+  pdl_entry();
   const int tok = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int pos = pos_of_tok[tok];
@@ -69,6 +70,7 @@ __global__ void kv_prep_kernel(const __nv_bfloat16* __restrict__ kva, long long 
                                int cache_mode /*0 none, 1 bf16, 2 nvfp4*/, uint8_t* __restrict__ cache,
                                __nv_bfloat16* __restrict__ lat_out, __nv_bfloat16* __restrict__ rope_out,
                                uint8_t* __restrict__ lat_q, uint8_t* __restrict__ lat_s, int* __restrict__ status) {
+  pdl_entry();
   const int tok = blockIdx.x;
   const __nv_bfloat16* src = kva + (size_t)tok * kva_stride;
   __shared__ float vals[1024];
@@ -168,7 +170,7 @@ void q_prep(torch::Tensor qb, int64_t Hh, int64_t nope, int64_t rope, torch::Ten
   long long qcs = 0; int qhs = 0;
   if (qcat.has_value() && qcat->defined()) { qcs = qcat->stride(0); qhs = qcat->stride(1); }
   const int warps = std::min<int>(8, Hh);
-  q_prep_kernel<<<dim3(T, (Hh + warps - 1) / warps), 32 * warps, 0, stream>>>((const __nv_bfloat16*)qb.data_ptr(), qb.stride(0), Hh, nope, rope,
+  launch_k(q_prep_kernel, dim3(T, (Hh + warps - 1) / warps), 32 * warps, 0, stream, (const __nv_bfloat16*)qb.data_ptr(), qb.stride(0), Hh, nope, rope,
                                                pos_of_tok.data_ptr<int>(), cos_sin.data_ptr<float>(),
                                                (uint8_t*)opt_ptr(qn_q), (uint8_t*)opt_ptr(qn_s),
                                                (__nv_bfloat16*)opt_ptr(qcat), qcs, qhs, (int)rope_off,
@@ -189,7 +191,7 @@ void kv_prep(torch::Tensor kva, int64_t lat, int64_t rope, torch::Tensor norm_w,
   if (cache_mode == 1) num_slots = cache->numel() / 584;
   if (cache_mode == 2) num_slots = cache->numel() / 352;
   auto stream = at::cuda::getCurrentCUDAStream();
-  kv_prep_kernel<<<T, 128, 0, stream>>>((const __nv_bfloat16*)kva.data_ptr(), kva.stride(0), lat, rope,
+  launch_k(kv_prep_kernel, T, 128, 0, stream, (const __nv_bfloat16*)kva.data_ptr(), kva.stride(0), lat, rope,
                                          (const __nv_bfloat16*)norm_w.data_ptr(), (float)eps,
                                          pos_of_tok.data_ptr<int>(), cos_sin.data_ptr<float>(),
                                          cache_mode ? (const long long*)slot_mapping->data_ptr<int64_t>() : nullptr, num_slots,

@@ -18,12 +18,14 @@ namespace moet {
 
 constexpr int kMaxE = 512;
 
-__global__ void router_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
-                                   int T, int E, int k, int sigmoid, int n_group, int topk_group,
-                                   int norm, float scaling, int* __restrict__ ids, float* __restrict__ wts) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= T) return;
-  constexpr int PER = kMaxE / 32;
+// Top-k of one token's router logits (one warp): sigmoid + selection bias (or
+// softmax), optional group limit, renormalised and scaled weights.
+// PER = values per lane (E <= 32 * PER); the k selection rounds cost O(PER).
+template <int PER>
+__device__ __forceinline__ void topk_token_t(const float* __restrict__ logits, const float* __restrict__ bias,
+                                             int warp, int E, int k, int sigmoid, int n_group, int topk_group,
+                                             int norm, float scaling, int* __restrict__ ids, float* __restrict__ wts) {
+  const int lane = threadIdx.x & 31;
   float score[PER], sel[PER];
   const int per = (E + 31) / 32;
   const float* lg = logits + (size_t)warp * E;
@@ -64,8 +66,8 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, const float
   if (n_group > 1 && topk_group < n_group) {
     // group score = sum of the two best selection scores in the group; keep topk_group groups
     const int gsize = E / n_group;
-    __shared__ float gscore_s[8][64];
-    float* gscore = gscore_s[threadIdx.x >> 5];
+    __shared__ float gscore_s[16][64];
+    float* gscore = gscore_s[(threadIdx.x >> 5) & 15];
     __syncwarp();
     // Compute group scores cooperatively: each lane owns experts lane+32i.
     for (int gi = 0; gi < n_group; gi++) {
@@ -137,11 +139,37 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, const float
   }
 }
 
+__device__ __forceinline__ void topk_token(const float* __restrict__ logits, const float* __restrict__ bias,
+                                           int warp, int E, int k, int sigmoid, int n_group, int topk_group,
+                                           int norm, float scaling, int* __restrict__ ids, float* __restrict__ wts) {
+  if (E <= 128)
+    topk_token_t<4>(logits, bias, warp, E, k, sigmoid, n_group, topk_group, norm, scaling, ids, wts);
+  else if (E <= 256)
+    topk_token_t<8>(logits, bias, warp, E, k, sigmoid, n_group, topk_group, norm, scaling, ids, wts);
+  else
+    topk_token_t<kMaxE / 32>(logits, bias, warp, E, k, sigmoid, n_group, topk_group, norm, scaling, ids, wts);
+}
+
+__global__ void router_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+                                   int T, int E, int k, int sigmoid, int n_group, int topk_group,
+                                   int norm, float scaling, int* __restrict__ ids, float* __restrict__ wts) {
+  pdl_entry();
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (warp >= T) return;
+  topk_token(logits, bias, warp, E, k, sigmoid, n_group, topk_group, norm, scaling, ids, wts);
+}
+
 // ---------------------------------------------------------------------------
 // Router logits: logits[t, e] = x[t, :] . W[e, :] with bf16 x and W, fp32 sums.
 // One warp per expert, 16-byte vector loads, 8 tokens per pass.
 __global__ void router_logits_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
                                      const __nv_bfloat16* __restrict__ w, int E, float* __restrict__ out) {
+  {  // router weights are immutable: prefetch this CTA's experts' rows before waiting on x
+    const int e0 = blockIdx.x * (blockDim.x >> 5), ne = min((int)(blockDim.x >> 5), E - e0);
+    const char* wb = reinterpret_cast<const char*>(w + (size_t)e0 * H);
+    for (int i = threadIdx.x; i < ne * H * 2 / 128; i += blockDim.x) prefetch_l2(wb + (size_t)i * 128);
+  }
+  pdl_entry();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x * (blockDim.x >> 5) + warp;
   if (e >= E) return;
@@ -180,11 +208,12 @@ __global__ void router_logits_kernel(const __nv_bfloat16* __restrict__ x, int T,
 //   pos_of[R]       routing r (= t*k + j) -> sorted row
 //   pairs[P] int4   {expert, first sorted row, n rows (<= MB), 0}
 //   n_pairs[1]
-__global__ void build_pairs_kernel(const int* __restrict__ topk_ids, int R, int k, int E, int MB,
-                                   int* __restrict__ rank_scratch, int* __restrict__ sorted_tok,
-                                   int* __restrict__ pos_of, int4* __restrict__ pairs,
-                                   int* __restrict__ n_pairs, int* __restrict__ status,
-                                   int pad = 0, int* __restrict__ n_rows = nullptr) {
+// Block-wide body (blockDim.x >= E, a multiple of 32).
+__device__ __forceinline__ void build_pairs_block(const int* __restrict__ topk_ids, int R, int k, int E, int MB,
+                                                  int* __restrict__ rank_scratch, int* __restrict__ sorted_tok,
+                                                  int* __restrict__ pos_of, int4* __restrict__ pairs,
+                                                  int* __restrict__ n_pairs, int* __restrict__ status,
+                                                  int pad, int* __restrict__ n_rows) {
   __shared__ int cnt[kMaxE];
   __shared__ int start[kMaxE];
   __shared__ int pstart[kMaxE];
@@ -242,6 +271,94 @@ __global__ void build_pairs_kernel(const int* __restrict__ topk_ids, int R, int 
   }
 }
 
+__global__ void build_pairs_kernel(const int* __restrict__ topk_ids, int R, int k, int E, int MB,
+                                   int* __restrict__ rank_scratch, int* __restrict__ sorted_tok,
+                                   int* __restrict__ pos_of, int4* __restrict__ pairs,
+                                   int* __restrict__ n_pairs, int* __restrict__ status,
+                                   int pad = 0, int* __restrict__ n_rows = nullptr) {
+  pdl_entry();
+  build_pairs_block(topk_ids, R, k, E, MB, rank_scratch, sorted_tok, pos_of, pairs, n_pairs, status, pad, n_rows);
+}
+
+// Decode routing in one launch: every CTA computes the router logits of 16
+// experts for all T tokens (bf16 x and W, fp32 sums; the weights are
+// prefetched before the dependency wait); the last CTA to finish (arrival
+// counter, self-resetting) runs the top-k of every token and builds the
+// expert pair list.
+constexpr int kRouteWarps = 16;
+__global__ void __launch_bounds__(kRouteWarps * 32) moe_route_fused_kernel(
+    const __nv_bfloat16* __restrict__ x, int T, int H, const __nv_bfloat16* __restrict__ w, int E,
+    float* __restrict__ logits, const float* __restrict__ bias, int k, int sigmoid, int n_group, int topk_group,
+    int norm, float scaling, int* __restrict__ ids, float* __restrict__ wts, int MB,
+    int* __restrict__ rank_scratch, int* __restrict__ sorted_tok, int* __restrict__ pos_of,
+    int4* __restrict__ pairs, int* __restrict__ n_pairs, int* __restrict__ counter, int* __restrict__ status) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * kRouteWarps + warp;
+  // The expert's weight row is immutable: its first 16 x 16 B per lane (H <= 4096
+  // entirely) go to registers before the dependency wait.
+  constexpr int kPre = 16;
+  const int nvec = H / 256;   // 16-byte vectors per lane
+  const __nv_bfloat16* wr = w + (size_t)min(e, E - 1) * H;
+  uint4 wv[kPre];
+#pragma unroll
+  for (int u = 0; u < kPre; u++)
+    if (u < nvec) wv[u] = __ldg(reinterpret_cast<const uint4*>(wr + u * 256 + lane * 8));
+  pdl_entry();
+  // tokens are staged through shared memory 4 at a time (all loads in flight at once)
+  extern __shared__ __align__(16) uint8_t route_smem[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(route_smem);   // [4][H]
+  for (int t0 = 0; t0 < T; t0 += 4) {
+    const int nt = min(4, T - t0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nt * H / 8; i += blockDim.x)
+      reinterpret_cast<uint4*>(xs)[i] = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t0 * H) + i);
+    __syncthreads();
+    if (e < E) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int u0 = 0; u0 < nvec; u0 += kPre) {
+#pragma unroll
+        for (int u = 0; u < kPre; u++) {
+          if (u0 + u >= nvec) break;
+          const uint4 wq = u0 == 0 ? wv[u] : __ldg(reinterpret_cast<const uint4*>(wr + (u0 + u) * 256 + lane * 8));
+          const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wq);
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            if (j < nt) {
+              const uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)j * H + (u0 + u) * 256 + lane * 8);
+              const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
+#pragma unroll
+              for (int i = 0; i < 4; i++) {
+                const float2 a = __bfloat1622float2(x2[i]), b = __bfloat1622float2(w2[i]);
+                acc[j] = fmaf(a.x, b.x, fmaf(a.y, b.y, acc[j]));
+              }
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float v = warp_sum(acc[j]);
+        if (lane == 0 && j < nt) logits[(size_t)(t0 + j) * E + e] = v;
+      }
+    }
+  }
+  __shared__ int last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(counter, 1) == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (int t = warp; t < T; t += kRouteWarps)
+    topk_token(logits, bias, t, E, k, sigmoid, n_group, topk_group, norm, scaling, ids, wts);
+  __syncthreads();
+  __threadfence_block();
+  build_pairs_block(ids, T * k, k, E, MB, rank_scratch, sorted_tok, pos_of, pairs, n_pairs, status, 0, nullptr);
+  if (threadIdx.x == 0) *counter = 0;
+}
+
 }  // namespace moet
 
 using namespace moet;
@@ -256,7 +373,7 @@ void router_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_
   if (T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   const int warps = 8;
-  router_topk_kernel<<<(T + warps - 1) / warps, warps * 32, 0, stream>>>(
+  launch_k(router_topk_kernel, (T + warps - 1) / warps, warps * 32, 0, stream, 
       logits.data_ptr<float>(), bias.has_value() && bias->defined() ? bias->data_ptr<float>() : nullptr,
       T, E, (int)k, sigmoid ? 1 : 0, (int)n_group, (int)topk_group, norm ? 1 : 0, (float)scaling,
       ids.data_ptr<int>(), wts.data_ptr<float>());
@@ -267,6 +384,7 @@ void router_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_
 __global__ void gather_rows_kernel(const uint8_t* __restrict__ src_q, const uint8_t* __restrict__ src_s, int K,
                                    long long src_stride, const int* __restrict__ idx, const int* __restrict__ n_rows,
                                    uint8_t* __restrict__ dst_q, uint8_t* __restrict__ dst_s, long long dst_stride) {
+  pdl_entry();
   const int r = blockIdx.x;
   if (r >= *n_rows) return;
   const int i = idx[r];
@@ -287,9 +405,34 @@ void gather_rows(torch::Tensor src_q, torch::Tensor src_s, torch::Tensor idx, to
   TORCH_CHECK(dst_q.size(0) >= R && dst_s.size(0) >= R, "gather_rows: destination too small");
   if (R == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  gather_rows_kernel<<<R, 128, 0, stream>>>((const uint8_t*)src_q.data_ptr(), (const uint8_t*)src_s.data_ptr(), K,
+  launch_k(gather_rows_kernel, R, 128, 0, stream, (const uint8_t*)src_q.data_ptr(), (const uint8_t*)src_s.data_ptr(), K,
                                             src_q.stride(0), idx.data_ptr<int>(), n_rows.data_ptr<int>(),
                                             (uint8_t*)dst_q.data_ptr(), (uint8_t*)dst_s.data_ptr(), dst_q.stride(0));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void moe_route_fused(torch::Tensor x, torch::Tensor w, torch::Tensor logits, c10::optional<torch::Tensor> bias,
+                     int64_t k, bool sigmoid, int64_t n_group, int64_t topk_group, bool norm, double scaling,
+                     torch::Tensor ids, torch::Tensor wts, int64_t MB, torch::Tensor rank_scratch,
+                     torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
+                     torch::Tensor counter, torch::Tensor status) {
+  const int T = x.size(0), H = x.size(1), E = w.size(0);
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.is_contiguous() &&
+              w.is_contiguous() && H % 256 == 0, "moe_route_fused: bf16 contiguous, H % 256 == 0");
+  TORCH_CHECK(E <= kRouteWarps * 32 && k <= 32 && n_group <= 64, "moe_route_fused: E <= 512, k <= 32");
+  TORCH_CHECK(pairs.size(0) >= (int64_t)T * k / MB + std::min<int64_t>(E, (int64_t)T * k), "moe_route_fused: pairs");
+  if (T == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const size_t smem = (size_t)4 * H * 2;
+  // static shared memory of the top-k / pair-list phases + the token stage exceed the 48 KiB default
+  cudaFuncSetAttribute(moe_route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_k(moe_route_fused_kernel, (E + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, smem, stream,
+           (const __nv_bfloat16*)x.data_ptr(), T, H, (const __nv_bfloat16*)w.data_ptr(), E, logits.data_ptr<float>(),
+           bias.has_value() && bias->defined() ? (const float*)bias->data_ptr<float>() : (const float*)nullptr,
+           (int)k, sigmoid ? 1 : 0, (int)n_group, (int)topk_group, norm ? 1 : 0, (float)scaling,
+           ids.data_ptr<int>(), wts.data_ptr<float>(), (int)MB, rank_scratch.data_ptr<int>(),
+           sorted_tok.data_ptr<int>(), pos_of.data_ptr<int>(), (int4*)pairs.data_ptr<int>(), n_pairs.data_ptr<int>(),
+           counter.data_ptr<int>(), status.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -299,7 +442,7 @@ void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out) {
               w.is_contiguous() && H % 256 == 0, "router_logits: bf16 contiguous, H % 256 == 0");
   if (T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  router_logits_kernel<<<(E + 7) / 8, 256, 0, stream>>>((const __nv_bfloat16*)x.data_ptr(), T, H,
+  launch_k(router_logits_kernel, (E + 7) / 8, 256, 0, stream, (const __nv_bfloat16*)x.data_ptr(), T, H,
                                                         (const __nv_bfloat16*)w.data_ptr(), E, out.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -315,7 +458,7 @@ void build_pairs_padded(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Te
   const int64_t P = R / MB + std::min<int64_t>(E, R);
   TORCH_CHECK(pairs.size(0) >= P && sorted_tok.size(0) >= P * MB, "build_pairs_padded: buffers too small");
   auto stream = at::cuda::getCurrentCUDAStream();
-  build_pairs_kernel<<<1, 1024, 0, stream>>>(topk_ids.data_ptr<int>(), R, k, (int)E, (int)MB,
+  launch_k(build_pairs_kernel, 1, 1024, 0, stream, topk_ids.data_ptr<int>(), R, k, (int)E, (int)MB,
                                              rank_scratch.data_ptr<int>(), sorted_tok.data_ptr<int>(),
                                              pos_of.data_ptr<int>(), (int4*)pairs.data_ptr<int>(),
                                              n_pairs.data_ptr<int>(), status.data_ptr<int>(), 1, n_rows.data_ptr<int>());
@@ -329,10 +472,10 @@ void build_pairs(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor ra
   TORCH_CHECK(E <= kMaxE, "build_pairs: E <= 512");
   TORCH_CHECK(pairs.size(0) >= R / MB + std::min<int64_t>(E, R), "build_pairs: pairs buffer too small");
   auto stream = at::cuda::getCurrentCUDAStream();
-  build_pairs_kernel<<<1, 1024, 0, stream>>>(topk_ids.data_ptr<int>(), R, k, (int)E, (int)MB,
+  launch_k(build_pairs_kernel, 1, 1024, 0, stream, topk_ids.data_ptr<int>(), R, k, (int)E, (int)MB,
                                              rank_scratch.data_ptr<int>(), sorted_tok.data_ptr<int>(),
                                              pos_of.data_ptr<int>(), (int4*)pairs.data_ptr<int>(),
-                                             n_pairs.data_ptr<int>(), status.data_ptr<int>());
+                                             n_pairs.data_ptr<int>(), status.data_ptr<int>(), 0, (int*)nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

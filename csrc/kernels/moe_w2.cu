@@ -38,6 +38,7 @@ struct W2Args {
 
 template <int NT>
 __global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Args p) {
+  pdl_entry();
   const int pi = blockIdx.y;
   if (pi >= *p.n_pairs) return;
   const int4 pr = p.pairs[pi];
@@ -149,6 +150,7 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int* __res
                                    const __nv_bfloat16* __restrict__ shared_out,
                                    __nv_bfloat16* __restrict__ out, float* __restrict__ out_f32,
                                    int ar_on, ArDesc ar) {
+  pdl_entry();
   const int tok = blockIdx.x;
   const unsigned long long epoch = ar_on ? ar_epoch(ar) : 0ull;
   __shared__ int pos[32];
@@ -222,9 +224,9 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
   const size_t smem = (size_t)wpc * 16 * (K / 32);
   TORCH_CHECK(smem <= 48 * 1024, "moe_w2_gemv: K too large for the shared scale stage");
   switch (rows_per_pair) {
-    case 8: moe_w2_gemv_kernel<1><<<grid, wpc * 32, smem, stream>>>(p); break;
-    case 16: moe_w2_gemv_kernel<2><<<grid, wpc * 32, smem, stream>>>(p); break;
-    case 32: moe_w2_gemv_kernel<4><<<grid, wpc * 32, smem, stream>>>(p); break;
+    case 8: launch_k(moe_w2_gemv_kernel<1>, grid, wpc * 32, smem, stream, p); break;
+    case 16: launch_k(moe_w2_gemv_kernel<2>, grid, wpc * 32, smem, stream, p); break;
+    case 32: launch_k(moe_w2_gemv_kernel<4>, grid, wpc * 32, smem, stream, p); break;
     default: TORCH_CHECK(false, "moe_w2_gemv: rows_per_pair must be 8/16/32");
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -244,7 +246,7 @@ void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::
   TORCH_CHECK(H % 4 == 0 && k <= 32, "moe_combine: H % 4, k <= 32");
   if (T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  moe_combine_kernel<<<dim3(T, (H + 1023) / 1024), 256, 0, stream>>>(y.data_ptr<float>(), pos_of.data_ptr<int>(), wts.data_ptr<float>(), k, H,
+  launch_k(moe_combine_kernel, dim3(T, (H + 1023) / 1024), 256, 0, stream, y.data_ptr<float>(), pos_of.data_ptr<int>(), wts.data_ptr<float>(), k, H,
                                             (const __nv_bfloat16*)opt_ptr(resid), (const __nv_bfloat16*)opt_ptr(shared_out),
                                             (__nv_bfloat16*)opt_ptr(out), (float*)opt_ptr(out_f32), ar_on, d);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

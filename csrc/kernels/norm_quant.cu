@@ -67,6 +67,7 @@ __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x_in,
                                      uint8_t* __restrict__ q0, uint8_t* __restrict__ s0,
                                      uint8_t* __restrict__ q1, uint8_t* __restrict__ s1,
                                      int in_stride, int ostride, int ar_on, ArDesc ar) {
+  pdl_entry();
   const int row = blockIdx.x;
   const int k0 = threadIdx.x * VEC;
   float v[VEC];
@@ -138,6 +139,7 @@ __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x_in,
 __global__ void swiglu_quant_kernel(const float* __restrict__ in, int I, float limit,
                                     const int* __restrict__ n_rows, int layout,
                                     uint8_t* __restrict__ q, uint8_t* __restrict__ s) {
+  pdl_entry();
   const int row = blockIdx.x;
   if (n_rows && row >= *n_rows) return;
   constexpr int VEC = 8;
@@ -160,6 +162,7 @@ __global__ void swiglu_quant_kernel(const float* __restrict__ in, int I, float l
 template <typename T>
 __global__ void quant_kernel(const T* __restrict__ x, int K, int in_stride, int layout,
                              uint8_t* __restrict__ q, uint8_t* __restrict__ s) {
+  pdl_entry();
   const int row = blockIdx.x;
   constexpr int VEC = 8;
   for (int k0 = threadIdx.x * VEC; k0 < K; k0 += blockDim.x * VEC) {
@@ -199,7 +202,7 @@ void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> add, c10::optio
                 "rmsnorm_quant: the all-reduce consumer writes x_out = x + sum of partials (no add)");
     TORCH_CHECK((int64_t)rows * H <= d.cap, "rmsnorm_quant: rows*H exceeds the all-reduce slot");
   }
-  kern<<<rows, threads, 0, stream>>>(
+  launch_k(kern, rows, threads, 0, stream, 
       (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)opt_ptr(add),
       (__nv_bfloat16*)opt_ptr(x_out), (const __nv_bfloat16*)w.data_ptr(), (float)eps, H,
       (__nv_bfloat16*)opt_ptr(y_out), (uint8_t*)opt_ptr(q0), (uint8_t*)opt_ptr(s0),
@@ -215,7 +218,7 @@ void swiglu_quant(torch::Tensor in, double limit, c10::optional<torch::Tensor> n
   if (rows == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   int threads = std::min(256, I / 8);
-  swiglu_quant_kernel<<<rows, threads, 0, stream>>>(in.data_ptr<float>(), I, (float)limit,
+  launch_k(swiglu_quant_kernel, rows, threads, 0, stream, in.data_ptr<float>(), I, (float)limit,
                                                     (const int*)opt_ptr(n_rows), (int)layout,
                                                     (uint8_t*)q.data_ptr(), (uint8_t*)s.data_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -228,11 +231,11 @@ void quant_fp8(torch::Tensor x, int64_t layout, torch::Tensor q, torch::Tensor s
   auto stream = at::cuda::getCurrentCUDAStream();
   int threads = std::min(256, K / 8);
   if (x.scalar_type() == at::kBFloat16)
-    quant_kernel<__nv_bfloat16><<<rows, threads, 0, stream>>>((const __nv_bfloat16*)x.data_ptr(), K,
+    launch_k(quant_kernel<__nv_bfloat16>, rows, threads, 0, stream, (const __nv_bfloat16*)x.data_ptr(), K,
                                                              (int)x.stride(0), (int)layout,
                                                              (uint8_t*)q.data_ptr(), (uint8_t*)s.data_ptr());
   else if (x.scalar_type() == at::kFloat)
-    quant_kernel<float><<<rows, threads, 0, stream>>>(x.data_ptr<float>(), K, (int)x.stride(0), (int)layout,
+    launch_k(quant_kernel<float>, rows, threads, 0, stream, x.data_ptr<float>(), K, (int)x.stride(0), (int)layout,
                                                      (uint8_t*)q.data_ptr(), (uint8_t*)s.data_ptr());
   else
     TORCH_CHECK(false, "quant_fp8: bf16 or f32 input");

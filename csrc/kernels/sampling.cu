@@ -16,6 +16,7 @@ template <typename T>
 __global__ void argmax_lse_kernel(const T* __restrict__ logits, long long stride, int V,
                                   int* __restrict__ ids, float* __restrict__ lse, float* __restrict__ maxv,
                                   int* __restrict__ status) {
+  pdl_entry();
   const int row = blockIdx.x;
   const T* x = logits + (size_t)row * stride;
   float bv = -INFINITY; int bi = 0x7fffffff;
@@ -68,6 +69,7 @@ __global__ void argmax_lse_kernel(const T* __restrict__ logits, long long stride
 __global__ void mtp_accept_kernel(const int* __restrict__ targets, const int* __restrict__ tokens, int B, int kp1,
                                   int* __restrict__ out_tokens, int* __restrict__ n_acc,
                                   const int* __restrict__ active) {
+  pdl_entry();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   int a = 0;
@@ -82,6 +84,7 @@ __global__ void mtp_accept_kernel(const int* __restrict__ targets, const int* __
 __global__ void mtp_finalize_kernel(const int* __restrict__ targets, const int* __restrict__ n_acc,
                                     const int* __restrict__ drafts, int B, int kp1, int* __restrict__ tokens,
                                     int* __restrict__ seq_pos, const int* __restrict__ active) {
+  pdl_entry();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   if (active && !active[b]) return;
@@ -100,6 +103,7 @@ __global__ void argmax_split_kernel(const T* __restrict__ logits, long long stri
                                     float* __restrict__ part, int* __restrict__ counter, int* __restrict__ ids,
                                     float* __restrict__ lse, int* __restrict__ status,
                                     float2* __restrict__ mv = nullptr, int id_offset = 0) {
+  pdl_entry();
   const int row = blockIdx.x, S = gridDim.y, sp = blockIdx.y;
   const int per = (V + S - 1) / S, lo = sp * per, hi = min(V, lo + per);
   const T* x = logits + (size_t)row * stride;
@@ -163,6 +167,7 @@ __global__ void argmax_split_kernel(const T* __restrict__ logits, long long stri
 // Vocab-parallel argmax merge: parts [W, R] of (max, id bits) from W ranks (ids
 // already global) -> ids[R]; ties go to the smaller id, as in the 1-rank argmax.
 __global__ void argmax_merge_kernel(const float2* __restrict__ parts, int W, int R, int* __restrict__ ids) {
+  pdl_entry();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= R) return;
   float M = -INFINITY; int I = 0x7fffffff;
@@ -190,11 +195,11 @@ void argmax_split(torch::Tensor logits, c10::optional<torch::Tensor> ids, c10::o
   dim3 grid(R, S);
   const int want = lse.has_value() && lse->defined();
   if (logits.scalar_type() == at::kFloat)
-    argmax_split_kernel<float><<<grid, 256, 0, stream>>>(logits.data_ptr<float>(), logits.stride(0), V, want,
+    launch_k(argmax_split_kernel<float>, grid, 256, 0, stream, logits.data_ptr<float>(), logits.stride(0), V, want,
         part.data_ptr<float>(), counter.data_ptr<int>(), (int*)opt_ptr(ids), (float*)opt_ptr(lse), (int*)opt_ptr(status),
         (float2*)opt_ptr(mv), (int)id_offset);
   else
-    argmax_split_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>((const __nv_bfloat16*)logits.data_ptr(),
+    launch_k(argmax_split_kernel<__nv_bfloat16>, grid, 256, 0, stream, (const __nv_bfloat16*)logits.data_ptr(),
         logits.stride(0), V, want, part.data_ptr<float>(), counter.data_ptr<int>(), (int*)opt_ptr(ids),
         (float*)opt_ptr(lse), (int*)opt_ptr(status), (float2*)opt_ptr(mv), (int)id_offset);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -207,7 +212,7 @@ void argmax_merge(torch::Tensor parts, torch::Tensor ids) {
   TORCH_CHECK(ids.numel() >= R, "argmax_merge: ids too small");
   if (R == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  argmax_merge_kernel<<<(R + 127) / 128, 128, 0, stream>>>((const float2*)parts.data_ptr(), W, R, ids.data_ptr<int>());
+  launch_k(argmax_merge_kernel, (R + 127) / 128, 128, 0, stream, (const float2*)parts.data_ptr(), W, R, ids.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -218,10 +223,10 @@ void argmax_lse(torch::Tensor logits, torch::Tensor ids, c10::optional<torch::Te
   if (R == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   if (logits.scalar_type() == at::kFloat)
-    argmax_lse_kernel<float><<<R, 1024, 0, stream>>>(logits.data_ptr<float>(), logits.stride(0), V, ids.data_ptr<int>(),
+    launch_k(argmax_lse_kernel<float>, R, 1024, 0, stream, logits.data_ptr<float>(), logits.stride(0), V, ids.data_ptr<int>(),
                                                      (float*)opt_ptr(lse), (float*)opt_ptr(maxv), (int*)opt_ptr(status));
   else
-    argmax_lse_kernel<__nv_bfloat16><<<R, 1024, 0, stream>>>((const __nv_bfloat16*)logits.data_ptr(), logits.stride(0), V,
+    launch_k(argmax_lse_kernel<__nv_bfloat16>, R, 1024, 0, stream, (const __nv_bfloat16*)logits.data_ptr(), logits.stride(0), V,
                                                              ids.data_ptr<int>(), (float*)opt_ptr(lse), (float*)opt_ptr(maxv),
                                                              (int*)opt_ptr(status));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -231,7 +236,7 @@ void mtp_accept(torch::Tensor targets, torch::Tensor tokens, torch::Tensor out_t
                 c10::optional<torch::Tensor> active) {
   const int B = targets.size(0), kp1 = targets.size(1);
   auto stream = at::cuda::getCurrentCUDAStream();
-  mtp_accept_kernel<<<(B + 127) / 128, 128, 0, stream>>>(targets.data_ptr<int>(), tokens.data_ptr<int>(), B, kp1,
+  launch_k(mtp_accept_kernel, (B + 127) / 128, 128, 0, stream, targets.data_ptr<int>(), tokens.data_ptr<int>(), B, kp1,
                                                          out_tokens.data_ptr<int>(), n_acc.data_ptr<int>(),
                                                          (const int*)opt_ptr(active));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -241,7 +246,7 @@ void mtp_finalize(torch::Tensor targets, torch::Tensor n_acc, torch::Tensor draf
                   torch::Tensor seq_pos, c10::optional<torch::Tensor> active) {
   const int B = targets.size(0), kp1 = targets.size(1);
   auto stream = at::cuda::getCurrentCUDAStream();
-  mtp_finalize_kernel<<<(B + 127) / 128, 128, 0, stream>>>(targets.data_ptr<int>(), n_acc.data_ptr<int>(),
+  launch_k(mtp_finalize_kernel, (B + 127) / 128, 128, 0, stream, targets.data_ptr<int>(), n_acc.data_ptr<int>(),
                                                            drafts.data_ptr<int>(), B, kp1, tokens.data_ptr<int>(),
                                                            seq_pos.data_ptr<int>(), (const int*)opt_ptr(active));
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -401,3 +401,68 @@ def test_argmax_split_matches_torch_twice(C, R, V):
         assert torch.equal(ids.cpu().long(), x.argmax(-1))
         assert rel(lse.cpu(), torch.logsumexp(x, -1)) < 1e-5
     assert int(cnt.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("T,E,k,MB", [(3, 256, 8, 8), (1, 16, 4, 8), (40, 64, 6, 16)])
+def test_moe_route_fused_matches_separate_kernels(C, T, E, k, MB):
+    g = torch.Generator().manual_seed(T * 7 + E)
+    H = 1024
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(E, H, generator=g) * 0.05).to(torch.bfloat16).to(DEV)
+    bias = (torch.randn(E, generator=g) * 0.1).to(DEV)
+    R = T * k
+    P = R // MB + min(E, R)
+
+    def bufs():
+        return dict(lg=torch.empty(T, E, device=DEV), ids=torch.empty(T, k, dtype=torch.int32, device=DEV),
+                    wts=torch.empty(T, k, device=DEV), rank=torch.empty(R, dtype=torch.int32, device=DEV),
+                    stok=torch.empty(R, dtype=torch.int32, device=DEV), posof=torch.empty(R, dtype=torch.int32, device=DEV),
+                    pairs=torch.empty(P, 4, dtype=torch.int32, device=DEV), np=torch.empty(1, dtype=torch.int32, device=DEV))
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    a = bufs()
+    C.router_logits(x, w, a["lg"])
+    C.router_topk(a["lg"], bias, k, True, 1, 1, True, 2.5, a["ids"], a["wts"])
+    C.build_pairs(a["ids"], E, MB, a["rank"], a["stok"], a["posof"], a["pairs"], a["np"], st)
+    b = bufs()
+    cnt = torch.zeros(1, dtype=torch.int32, device=DEV)
+    for _ in range(2):       # replayable: the arrival counter resets itself
+        C.moe_route_fused(x, w, b["lg"], bias, k, True, 1, 1, True, 2.5, b["ids"], b["wts"], MB, b["rank"],
+                          b["stok"], b["posof"], b["pairs"], b["np"], cnt, st)
+    torch.cuda.synchronize()
+    assert int(st) == 0 and int(cnt) == 0
+    assert torch.allclose(a["lg"], b["lg"], rtol=1e-5, atol=1e-5)
+    assert torch.equal(a["ids"], b["ids"]) and torch.allclose(a["wts"], b["wts"])
+    n = int(a["np"])
+    assert n == int(b["np"])
+    # pair lists: same experts and row counts; every routing maps to a row of its expert with its token
+    assert torch.equal(a["pairs"][:n, [0, 2]], b["pairs"][:n, [0, 2]])
+    ids = b["ids"].view(-1).cpu(); posof = b["posof"].cpu(); stok = b["stok"].cpu(); pairs = b["pairs"][:n].cpu()
+    for r in range(R):
+        row = int(posof[r])
+        assert int(stok[row]) == r // k
+        pe = [p for p in pairs.tolist() if p[1] <= row < p[1] + p[2]]
+        assert len(pe) == 1 and pe[0][0] == int(ids[r])
+
+
+@pytest.mark.parametrize("T,Hh,S", [(3, 32, 8), (20, 4, 3)])
+def test_mla_combine_uv(C, T, Hh, S):
+    g = torch.Generator().manual_seed(T + Hh)
+    op = torch.randn(S, T, Hh, 512, generator=g)
+    ml = torch.stack([torch.randn(S, T, Hh, generator=g), torch.rand(S, T, Hh, generator=g) + 0.5], -1)
+    ml[S - 1, 0, 0, 0] = float("-inf")      # an empty split
+    wuv = torch.randn(Hh, 128, 512, generator=g) * 0.05
+    from vllm_moet_b200.models.weights import Fp8Linear
+    lins = [Fp8Linear.from_float(wuv[h]) for h in range(Hh)]
+    W = torch.stack([l.w for l in lins]); SW = torch.stack([l.s for l in lins])
+    q = torch.empty(T, Hh * 128, dtype=torch.uint8, device=DEV)
+    qs = torch.empty(T, Hh * 2, dtype=torch.uint8, device=DEV)
+    C.mla_combine_uv(op.to(DEV), ml.contiguous().to(DEV), W.to(DEV), SW.to(DEV), q, qs)
+    # reference: exact split merge (base-2 exponent state), then the dequantised W_uv
+    m, l = ml[..., 0], ml[..., 1]
+    M = m.max(0).values
+    e = torch.where(torch.isinf(m), torch.zeros_like(m), torch.exp2(m - M))
+    olat = (e[..., None] * op).sum(0) / (e * l).sum(0)[..., None]              # [T, Hh, 512]
+    wd = torch.stack([l.dequant() for l in lins])                             # [Hh, 128, 512]
+    ref = torch.einsum("thk,hjk->thj", olat, wd).reshape(T, Hh * 128)
+    got = fp8.dequant_act_fp8(q.cpu().view(torch.float8_e4m3fn), qs.cpu())
+    assert rel(got, ref) < 4e-2

@@ -107,8 +107,10 @@ class NativeRunner:
         self._pend = None         # (residual, out) of a pushed reduction the next RMSNorm completes
         self._fused = False
         self.nsplit = 8
+        self._side = torch.cuda.Stream(device=self.dev)   # second graph branch for independent chains
         import os
         self.debug_finite = os.environ.get("MOET_DEBUG_FINITE", "0") == "1"
+        self.branches = os.environ.get("MOET_BRANCHES", "1") != "0"
 
     # ------------------------------------------------------------------ helpers
     @staticmethod
@@ -212,6 +214,20 @@ class NativeRunner:
             self._tp_allreduce(part)
             torch.add(x, part, out=out)
 
+    def _fork(self):
+        """Start a side branch: work issued under the returned context runs
+        concurrently with the main stream (a parallel branch when captured into
+        the CUDA graph).  MOET_BRANCHES=0 keeps everything on one stream."""
+        if not self.branches:
+            import contextlib
+            return contextlib.nullcontext()
+        self._side.wait_stream(torch.cuda.current_stream())
+        return torch.cuda.stream(self._side)
+
+    def _join(self):
+        if self.branches:
+            torch.cuda.current_stream().wait_stream(self._side)
+
     # ------------------------------------------------------------------ layer
     def _attention(self, lw: LayerWeights, x, ctx: StepCtx, cache, li, out):
         cfg, C, T, Hh = self.cfg, self.C, ctx.T, self.Hh
@@ -221,30 +237,28 @@ class NativeRunner:
         qkva = self.ws.get("qkva", (T, ql + lat + rope), torch.bfloat16)
         self._gemv(hq, hs, lw.qkv_a, qkva)
         qaq, qas = self._fp8("qa", T, ql)
+        ovq, ovs = self._fp8("ov", T, Hh * vd)
+        if ctx.mode == "decode":
+            with self._fork():     # latent KV path (norm, rope, cache write) beside the query path
+                C.kv_prep(qkva[:, ql:], lat, rope, lw.kv_a_norm, cfg.rms_eps, ctx.pos, self.cos_sin, ctx.slot,
+                          self.kv_mode, cache, None, None, None, None, self.status)
         C.rmsnorm_quant(qkva[:, :ql], None, None, lw.q_a_norm, cfg.rms_eps, None, qaq, qas, None, None, 0)
         qb = self.ws.get("qb", (T, Hh * (nope + rope)), torch.bfloat16)
         self._gemv(qaq, qas, lw.q_b, qb)
-        ovq, ovs = self._fp8("ov", T, Hh * vd)
         if ctx.mode == "decode":
-            C.kv_prep(qkva[:, ql:], lat, rope, lw.kv_a_norm, cfg.rms_eps, ctx.pos, self.cos_sin, ctx.slot,
-                      self.kv_mode, cache, None, None, None, None, self.status)
             qnq = self.ws.get("qn.q", (T, Hh, nope), torch.uint8)
             qns = self.ws.get("qn.s", (T, Hh, nope // 64), torch.uint8)
             qcat = self.ws.get("qcat", (T, Hh, lat + rope), torch.bfloat16)
             C.q_prep(qb, Hh, nope, rope, ctx.pos, self.cos_sin, qnq, qns, qcat, lat, None)
             C.gemv_fp8(qnq.permute(1, 0, 2), qns.permute(1, 0, 2), lw.w_uk_t.w, lw.w_uk_t.s,
                        qcat[:, :, :lat].permute(1, 0, 2), None)
+            self._join()
             S = max(1, min(32, 256 // T))
             opart = self.ws.get("opart", (S, T, Hh, lat), torch.float32)
             mlp = self.ws.get("mlpart", (S, T, Hh, 2), torch.float32)
             C.mla_decode(qcat, cache, ctx.block_table, ctx.seq, ctx.pos, opart, mlp, self.scale, self.status)
-            olq = self.ws.get("ol.q", (T, Hh, lat), torch.uint8)
-            ols = self.ws.get("ol.s", (T, Hh, lat // 64), torch.uint8)
-            C.mla_combine(opart, mlp, None, olq, ols)
-            ov = self.ws.get("ov", (T, Hh * vd), torch.bfloat16)
-            C.gemv_fp8(olq.permute(1, 0, 2), ols.permute(1, 0, 2), lw.w_uv.w, lw.w_uv.s,
-                       ov.view(T, Hh, vd).permute(1, 0, 2), None)
-            C.quant_fp8(ov, 0, ovq, ovs)
+            # split merge + W_uv + e4m3 quantisation in one kernel
+            C.mla_combine_uv(opart, mlp, lw.w_uv.w, lw.w_uv.s, ovq, ovs)
         else:
             latq, lats = self._fp8("lat", T, lat)
             kr = self.ws.get("kr", (T, rope), torch.bfloat16)
@@ -274,33 +288,52 @@ class NativeRunner:
             return
         h2q, h2s = self._fp8("h2", T, H)
         self._norm_in(x, lw.ffn_norm, hb, hq, hs, h2q, h2s)
+        sh = None
+        if lw.shared_gate_up is not None:
+            with self._fork():     # shared expert beside the router and the routed experts
+                Is2 = lw.shared_gate_up.w.shape[0]
+                sgu = self.ws.get("sgu", (T, Is2), torch.float32)
+                self._gemv(hq, hs, lw.shared_gate_up, sgu)
+                sq, ss = self._fp8("sact", T, Is2 // 2)
+                C.swiglu_quant(sgu, cfg.swiglu_limit or 0.0, None, 0, sq, ss)
+                sh = self.ws.get("sh", (T, H), torch.bfloat16)
+                self._gemv(sq, ss, lw.shared_down, sh)
         E, k = cfg.num_experts, cfg.top_k
         logits = self.ws.get("rlogits", (T, E), torch.float32)
-        if T <= 64:
-            C.router_logits(hb, self._router_w(lw), logits)
-        else:   # prefill: a plain GEMM, cuBLAS in fp32
-            torch.mm(hb.float(), lw.router_w.t(), out=logits)
         ids = self.ws.get("topk_ids", (T, k), torch.int32)
         wts = self.ws.get("topk_w", (T, k), torch.float32)
-        C.router_topk(logits, lw.router_bias, k, cfg.router == "sigmoid", cfg.n_group, cfg.topk_group,
-                      cfg.norm_topk_prob, cfg.routed_scaling, ids, wts)
         R = T * k
         ex = lw.experts
         L = ex.layout
         I = L.I
-        if ctx.mode == "prefill" and H % 128 == 0 and I % 128 == 0 and (2 * I) % 128 == 0:
-            y2, posof = self._moe_tc(h2q, h2s, ids, ex, R, T)
+        use_tc = ctx.mode == "prefill" and H % 128 == 0 and I % 128 == 0 and (2 * I) % 128 == 0
+        if T <= 64 and not use_tc:
+            # decode: logits + top-k + pair list in one launch
+            MB = ctx.mb
+            P = R // MB + min(E, R)
+            rank = self.ws.get("rank", (R,), torch.int32)
+            stok = self.ws.get("stok", (R,), torch.int32)
+            posof = self.ws.get("posof", (R,), torch.int32)
+            pairs = self.ws.get("pairs", (P, 4), torch.int32)
+            npairs = self.ws.get("npairs", (1,), torch.int32)
+            cnt = self.ws.zeros("route.cnt", (1,), torch.int32)
+            C.moe_route_fused(hb, self._router_w(lw), logits, lw.router_bias, k, cfg.router == "sigmoid",
+                              cfg.n_group, cfg.topk_group, cfg.norm_topk_prob, cfg.routed_scaling, ids, wts, MB,
+                              rank, stok, posof, pairs, npairs, cnt, self.status)
+            y2 = self._moe_gemv_pairs(h2q, h2s, stok, pairs, npairs, ex, R, MB)
         else:
-            y2, posof = self._moe_gemv(h2q, h2s, ids, ex, R, ctx.mb)
-        sh = None
-        if lw.shared_gate_up is not None:
-            Is2 = lw.shared_gate_up.w.shape[0]
-            sgu = self.ws.get("sgu", (T, Is2), torch.float32)
-            self._gemv(hq, hs, lw.shared_gate_up, sgu)
-            sq, ss = self._fp8("sact", T, Is2 // 2)
-            C.swiglu_quant(sgu, cfg.swiglu_limit or 0.0, None, 0, sq, ss)
-            sh = self.ws.get("sh", (T, H), torch.bfloat16)
-            self._gemv(sq, ss, lw.shared_down, sh)
+            if T <= 64:
+                C.router_logits(hb, self._router_w(lw), logits)
+            else:   # prefill: a plain GEMM, cuBLAS in fp32
+                torch.mm(hb.float(), lw.router_w.t(), out=logits)
+            C.router_topk(logits, lw.router_bias, k, cfg.router == "sigmoid", cfg.n_group, cfg.topk_group,
+                          cfg.norm_topk_prob, cfg.routed_scaling, ids, wts)
+            if use_tc:
+                y2, posof = self._moe_tc(h2q, h2s, ids, ex, R, T)
+            else:
+                y2, posof = self._moe_gemv(h2q, h2s, ids, ex, R, ctx.mb)
+        if sh is not None:
+            self._join()
         if self.tp_group is None:
             C.moe_combine(y2, posof, wts, x, sh, out, None)
         elif self._fused:
@@ -356,6 +389,13 @@ class NativeRunner:
         pairs = self.ws.get("pairs", (P, 4), torch.int32)
         npairs = self.ws.get("npairs", (1,), torch.int32)
         C.build_pairs(ids, E, MB, rank, stok, posof, pairs, npairs, self.status)
+        return self._moe_gemv_pairs(h2q, h2s, stok, pairs, npairs, ex, R, MB), posof
+
+    def _moe_gemv_pairs(self, h2q, h2s, stok, pairs, npairs, ex, R, MB):
+        C, cfg = self.C, self.cfg
+        H = cfg.hidden
+        L = ex.layout
+        I = L.I
         c13 = self.ws.get("c13", (R, 2 * I), torch.float32)
         C.moe_w2_gemv(h2q, h2s, stok, pairs, npairs, ex.pool, L.off_codes13, L.off_sc13, ex.slot_table, c13,
                       2 * I, H, MB, self.miss)
@@ -364,7 +404,7 @@ class NativeRunner:
         y2 = self.ws.get("y2", (R, H), torch.float32)
         C.moe_w2_gemv(a2q, a2s, None, pairs, npairs, ex.pool, L.off_codes2, L.off_sc2, ex.slot_table, y2,
                       H, I, MB, self.miss)
-        return y2, posof
+        return y2
 
     def _check(self, name, t):
         """Debug aid (MOET_DEBUG_FINITE=1, eager only): raise at the first non-finite stage output."""
@@ -553,9 +593,10 @@ class NativeRunner:
             prev_tok = dj
         C.mtp_finalize(st.targets, st.n_acc, st.drafts, st.tokens, st.seq_pos, st.active)
 
-    def capture(self, st):
+    def capture(self, st, warm: bool = True):
         """Capture decode_body for the state's batch bucket (after one eager warm-up)."""
-        self.decode_body_eager_warm(st)
+        if warm:
+            self.decode_body_eager_warm(st)
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
