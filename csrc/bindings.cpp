@@ -1,6 +1,8 @@
 // Python bindings of the vllm_moet_b200 native library (_C).
 #include <torch/extension.h>
 
+// runtime/pack_io.cpp
+void register_pack_io(pybind11::module& m);
 // norm_quant.cu
 void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> add, c10::optional<torch::Tensor> x_out,
                    torch::Tensor w, double eps, c10::optional<torch::Tensor> y_out,
@@ -103,6 +105,7 @@ void ws_gemm_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tens
                  c10::optional<torch::Tensor> resid, int64_t T, torch::Tensor status);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  register_pack_io(m);
   m.doc() = "vllm_moet_b200 sm_100a kernels";
   m.def("rmsnorm_quant", &rmsnorm_quant, py::arg("x"), py::arg("add"), py::arg("x_out"), py::arg("w"), py::arg("eps"),
         py::arg("y_out"), py::arg("q0"), py::arg("s0"), py::arg("q1"), py::arg("s1"), py::arg("ostride"),

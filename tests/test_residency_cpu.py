@@ -1,0 +1,258 @@
+"""Residency tiers on the CPU: host stores (byte identity across backends,
+cold / warm / reboot / evict / overflow / scan / preheat, injected read
+faults, concurrent writers), planes cache identity, the expert cache's slot
+policy and fail-closed fetch, miss replay to a fixed point (1 rank and a
+2-rank gloo consensus), the confidence gate, the speculation guard and the
+pool floors."""
+import os
+
+import pytest
+import torch
+
+from mp_util import run_ranks
+from vllm_moet_b200.residency import (ConfidenceGate, DraftAffinity, ExpertCache, FetchError, LookaheadPrefetcher,
+                                      PlanesCache, ReplayEngine, SpecGuard, gate_fire_floor, make_store,
+                                      pack_has_layer, working_set_floor)
+from vllm_moet_b200.residency.stores import pack_paths
+
+L, E, SB = 3, 8, 5000
+
+
+def layer_rows(li, seed=0):
+    g = torch.Generator().manual_seed(seed * 100 + li)
+    return torch.randint(0, 256, (E, SB), generator=g, dtype=torch.uint8)
+
+
+def fill(store, layers=range(L)):
+    for li in layers:
+        store.add_layer(li, layer_rows(li))
+
+
+@pytest.mark.parametrize("kind", ["pinned", "pack", "tiered"])
+def test_backends_byte_identical(tmp_path, kind):
+    st = make_store(kind, L, E, SB, dir=str(tmp_path), ckpt_id="t", arena_rows=5)
+    fill(st)
+    for li in range(L):
+        want = layer_rows(li)
+        for experts in ([0, 3, 7], [7, 0], [1, 2, 3, 4, 5, 6]):
+            b = st.rows_for(li, experts)
+            assert not b.failed
+            for e, r in zip(experts, b.rows):
+                assert torch.equal(r, want[e]), (kind, li, e)
+
+
+def test_pack_reboot_and_identity(tmp_path):
+    d = str(tmp_path)
+    st = make_store("pack", L, E, SB, dir=d, ckpt_id="ck1")
+    fill(st, [0, 2])
+    st.release()
+    assert pack_has_layer(d, "base", L, E, SB, 0, ckpt_id="ck1")
+    assert not pack_has_layer(d, "base", L, E, SB, 1, ckpt_id="ck1")
+    assert not pack_has_layer(d, "base", L, E, SB, 0, ckpt_id="other")   # another checkpoint never matches
+    st2 = make_store("pack", L, E, SB, dir=d, ckpt_id="ck1")              # "reboot"
+    assert st2.has_layer(0) and st2.has_layer(2) and not st2.has_layer(1)
+    assert torch.equal(st2.rows_for(2, [5]).rows[0], layer_rows(2)[5])
+    pack, side, _, _ = pack_paths(d, "base", L, E, SB, "ck1")
+    assert os.path.getsize(pack) >= 3 * E * 8192 - 8192     # rows at (li*E+e)*stride, 4 KiB stride
+    with open(side, "w") as f:
+        f.write("{corrupt")
+    st3 = make_store("pack", L, E, SB, dir=d, ckpt_id="ck1")              # corrupt sidecar -> rebuild
+    assert not st3.has_layer(0)
+
+
+def test_tiered_evict_scan_and_preheat(tmp_path):
+    st = make_store("tiered", L, E, SB, dir=str(tmp_path), ckpt_id="t", arena_rows=4)
+    fill(st)
+    st.rows_for(0, [0, 1, 2, 3])
+    assert st.stats()["arena_misses"] == 4
+    st.rows_for(0, [0, 1])
+    assert st.stats()["arena_hits"] == 2
+    st.rows_for(1, [0])                     # evicts the LRU row (0, 2)
+    assert st.stats()["arena_evictions"] == 1 and (0, 2) not in st.lru
+    before = dict(st.lru)
+    b = st.rows_for(2, [0, 1, 2, 3, 4, 5], scan=True)   # a sweep larger than the arena: no pollution
+    assert not b.failed and dict(st.lru) == before
+    assert torch.equal(b.rows[5], layer_rows(2)[5])
+    b = st.rows_for(2, [6], scan=True)
+    assert (2, 6) not in st.lru
+    st.dump_heat()
+    st2 = make_store("tiered", L, E, SB, dir=str(tmp_path), ckpt_id="t", arena_rows=4)
+    assert st2.preheat() >= 3
+    assert st2.rows_for(1, [0]).rows[0] is not None and st2.stats()["arena_hits"] >= 1
+
+
+def test_injected_read_faults_never_publish(tmp_path):
+    st = make_store("tiered", L, E, SB, dir=str(tmp_path), ckpt_id="t", arena_rows=6)
+    fill(st)
+    st.inject_read_faults(2)                # every 2nd read fails with EIO
+    b = st.rows_for(0, [0, 1, 2, 3])
+    assert len(b.failed) == 2
+    for e, r in zip([0, 1, 2, 3], b.rows):
+        assert (r is None) == (e in b.failed)
+        if r is not None:
+            assert torch.equal(r, layer_rows(0)[e])
+    for e in b.failed:
+        assert (0, e) not in st.lru         # a failed read is not in the arena
+    st.inject_read_faults(0)
+    b2 = st.rows_for(0, b.failed)
+    assert not b2.failed and all(torch.equal(r, layer_rows(0)[e]) for e, r in zip(b.failed, b2.rows))
+
+
+def _writer(rank, world, d):
+    st = make_store("pack", L, E, SB, dir=d, ckpt_id="mp", suffix="rank0of1")
+    st.add_layer(rank, layer_rows(rank))
+    return sorted(st.layers)
+
+
+def test_concurrent_writers_share_one_sidecar(tmp_path):
+    run_ranks(_writer, 2, str(tmp_path))
+    st = make_store("pack", L, E, SB, dir=str(tmp_path), ckpt_id="mp", suffix="rank0of1")
+    assert st.has_layer(0) and st.has_layer(1)
+    assert torch.equal(st.rows_for(1, [4]).rows[0], layer_rows(1)[4])
+
+
+def test_planes_cache(tmp_path):
+    pc = PlanesCache(str(tmp_path), "ck", tp_world=2, tp_rank=1)
+    parts = {"codes13": torch.arange(100, dtype=torch.uint8), "sc13": torch.ones(7, dtype=torch.uint8)}
+    assert pc.try_load(0, {"codes13": 100, "sc13": 7}) is None
+    pc.store(0, parts)
+    pc.flush()
+    got = pc.try_load(0, {"codes13": 100, "sc13": 7})
+    assert got is not None and torch.equal(got["codes13"], parts["codes13"])
+    assert pc.try_load(0, {"codes13": 101, "sc13": 7}) is None        # exact sizes required
+    assert "tp2-rank1" in pc.rank_dir and os.path.exists(os.path.join(pc.base, "meta.json"))
+    pc2 = PlanesCache(str(tmp_path), "other-ckpt", tp_world=2, tp_rank=1)
+    assert pc2.base != pc.base and pc2.try_load(0, {"codes13": 100, "sc13": 7}) is None
+    assert PlanesCache(str(tmp_path), None).try_load(0, {"codes13": 100}) is None   # unverified: never cached
+    pc.close()
+
+
+def _cache(tmp_path, slots=6, policy="lru"):
+    st = make_store("pinned", L, E, SB)
+    fill(st)
+    return ExpertCache(st, L, E, SB, slots, device="cpu", policy=policy, manager=False)
+
+
+def test_expert_cache_promote_evict_pin(tmp_path):
+    c = _cache(tmp_path)
+    assert c.promote([(0, 1), (0, 2), (1, 3)]) == 3
+    assert int(c.slot_table[0, 1]) >= 0 and torch.equal(c.pool[int(c.slot_table[0, 1])], layer_rows(0)[1])
+    c.step_end()
+    c.promote([(2, 0), (2, 1), (2, 2)])      # fills the pool
+    c.step_end()
+    c.note_routed(0, [1])                    # pinned for this step
+    c.promote([(1, 7)])                      # evicts an unpinned slot, never (0, 1)
+    assert c.resident(0, 1) and c.resident(1, 7) and c.stats["evictions"] == 1
+    for li in range(L):
+        for e in range(E):
+            s = int(c.slot_table[li, e])
+            assert (s >= 0) == c.resident(li, e)
+            if s >= 0:
+                assert torch.equal(c.pool[s], layer_rows(li)[e])
+    with pytest.raises(FetchError):
+        c.promote([(li, e) for li in range(L) for e in range(E)])   # more than the pool
+
+
+def test_failed_fetch_publishes_nothing(tmp_path):
+    st = make_store("pack", L, E, SB, dir=str(tmp_path), ckpt_id="f")
+    fill(st)
+    c = ExpertCache(st, L, E, SB, 8, device="cpu", manager=False)
+    st.inject_read_faults(3)
+    with pytest.raises(FetchError):
+        c.promote([(0, 0), (0, 1), (0, 2), (0, 3)])
+    assert int((c.slot_table >= 0).sum()) == 0 and c.stats["fetch_failures"] >= 1
+
+
+class FakeModel:
+    """A "step" routes fixed experts per layer; the fake kernel counts routed experts
+    whose slot is -1 into miss_count (what the native expert GEMVs do in-graph)."""
+
+    def __init__(self, cache, routes):
+        self.cache, self.routes, self.state, self.outputs = cache, routes, 0, []
+
+    def step(self):
+        for li, ids in enumerate(self.routes):
+            self.cache.miss_count += int((self.cache.slot_table[li, ids] < 0).sum())
+        self.outputs.append(self.state)
+        self.state += 1
+
+    def restore(self):
+        self.state -= 1
+
+
+def test_replay_converges_single_rank(tmp_path):
+    c = _cache(tmp_path, slots=12)
+    routes = [torch.tensor([0, 1]), torch.tensor([2, 3, 4]), torch.tensor([5])]
+    m = FakeModel(c, routes)
+    r = ReplayEngine(c, fp_max=4)
+    assert r.run(m.step, m.restore, lambda: routes) == 1      # one replay after fetching all 6
+    assert m.outputs == [0, 0] and m.state == 1
+    assert r.run(m.step, m.restore, lambda: routes) == 0      # warm: no replay
+    c2 = _cache(tmp_path, slots=12)
+    with pytest.raises(RuntimeError):
+        ReplayEngine(c2, fp_max=0).run(FakeModel(c2, routes).step, lambda: None, lambda: routes)
+
+
+def _replay_rank(rank, world):
+    import torch.distributed as dist
+    st = make_store("pinned", L, E, SB)
+    fill(st)
+    c = ExpertCache(st, L, E, SB, 12, device="cpu", manager=False)
+    if rank == 1:
+        c.promote([(0, 0)])      # ranks start with different caches
+        c.step_end()
+    routes = [torch.tensor([0, 1]), torch.tensor([2]), torch.tensor([3 + rank])]   # rank-specific routing
+    m = FakeModel(c, routes)
+    r = ReplayEngine(c, tp_group=dist.group.WORLD, fp_max=4, comm_device="cpu")
+    n = r.run(m.step, m.restore, lambda: routes)
+    return n, sorted(map(tuple, (c.slot_table >= 0).nonzero().tolist()))
+
+
+def test_replay_tp_consensus_gloo():
+    (n0, res0), (n1, res1) = run_ranks(_replay_rank, 2)
+    assert n0 == n1 == 1                       # both ranks replay the same number of times
+    assert res0 == res1                        # and fetched the union of the missing sets
+    assert (2, 3) in res0 and (2, 4) in res0
+
+
+def test_confidence_gate_and_floors():
+    g = ConfidenceGate(tau=0.5)
+    sure = torch.tensor([[10.0, 0.0, 0.0]])
+    unsure = torch.tensor([[1.0, 1.0, 0.9]])
+    assert g.score(sure) > 0.99 and g.score(unsure) < 0.5
+    calls = {"promote": 0, "restore": 0}
+    logits = [unsure, sure]
+    n = g.run(lambda: logits[min(calls["restore"], 1)], lambda: calls.__setitem__("restore", calls["restore"] + 1),
+              lambda: [(0, 1)], lambda p: calls.__setitem__("promote", calls["promote"] + 1) or 1)
+    assert n == 1 and calls == {"promote": 1, "restore": 1}
+    gm = ConfidenceGate(tau=0.2, signal="margin", agg="q0.5")
+    assert gm.score(torch.tensor([[5.0, 0.0], [0.0, 0.0]])) < 0.6
+    assert working_set_floor(31, 8, 2, 1) == int(1.15 * 31 * 8 * 3 + 0.999)
+    assert gate_fire_floor(31, 8, 3, 3) >= 31 * 8 * 3
+
+
+def test_spec_guard_latch_and_resume():
+    sg = SpecGuard(alpha=0.5, patience=4)
+    allowed = [sg.observe(True) for _ in range(4)]
+    assert allowed[-1] is False and sg.suppressed
+    for _ in range(6):
+        sg.observe(False)
+    assert not sg.suppressed
+    sg2 = SpecGuard(alpha=0.5, patience=2)
+    for _ in range(20):
+        sg2.observe(True)
+    assert sg2.backoff > 1                     # suppression that does not warm the pool backs off
+
+
+def test_prefetchers(tmp_path):
+    c = _cache(tmp_path, slots=16)
+    routers = [None, torch.eye(E)[:, :4].repeat(1, 1)[:E, :4].t().contiguous().float().repeat(1, 1), None]
+    routers[1] = torch.randn(E, 4)
+    lp = LookaheadPrefetcher(c, routers, top_k=2, extra=0)
+    h = torch.randn(1, 4)
+    want = {(1, int(e)) for e in torch.topk(h @ routers[1].t(), 2).indices.view(-1)}
+    lp.step(0, h)
+    assert all(c.resident(*p) for p in want)
+    da = DraftAffinity(c)
+    da.record([42], [torch.tensor([[5]]), None, torch.tensor([[6]])])
+    assert da.prefetch([42]) == 2 and c.resident(0, 5) and c.resident(2, 6)

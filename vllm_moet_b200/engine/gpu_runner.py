@@ -104,6 +104,8 @@ class NativeRunner:
         self.tp_group = None
         self.tp_rank, self.tp_size = mw.tp_rank, mw.tp_size
         self.ar = None            # fused peer-memory all-reduce (SymmAllReduce) for decode-sized steps
+        self.cache = None         # residency.ExpertCache when routed experts are served from a host store
+        self._moe_index = {}
         self._pend = None         # (residual, out) of a pushed reduction the next RMSNorm completes
         self._fused = False
         self.nsplit = 8
@@ -185,6 +187,26 @@ class NativeRunner:
         if fused and group is not None:
             from ..parallel.symm import SymmAllReduce
             self.ar = SymmAllReduce(group, 128 * self.cfg.hidden, self.dev, self.status)
+
+    def attach_expert_cache(self, cache):
+        """Serve routed experts through `cache` (pools already rewired by
+        residency.build_expert_cache).  Kernels count misses into cache.miss_count;
+        every MoE layer keeps its own routing buffer so misses can be fetched."""
+        from ..residency import moe_layers
+        self.cache = cache
+        self.miss = cache.miss_count
+        self._moe_index = {id(lw): i for i, lw in enumerate(moe_layers(self.mw))}
+
+    def route_ids(self, B: int):
+        """Per-MoE-layer routed expert ids of the last decode step of bucket B."""
+        ws = self._bucket_ws(B)
+        return [ws.bufs.get((f"topk_ids.{i}", torch.int32)) for i in range(len(self._moe_index))]
+
+    def _ensure_experts(self, li, ids):
+        """Eager passes (prefill, un-captured decode): fetch this layer's routed experts now."""
+        if self.cache is None or li is None or torch.cuda.is_current_stream_capturing():
+            return
+        self.cache.ensure_resident(li, torch.unique(ids).tolist())
 
     def _tp_allreduce(self, t):
         if self.tp_group is not None:
@@ -300,7 +322,8 @@ class NativeRunner:
                 self._gemv(sq, ss, lw.shared_down, sh)
         E, k = cfg.num_experts, cfg.top_k
         logits = self.ws.get("rlogits", (T, E), torch.float32)
-        ids = self.ws.get("topk_ids", (T, k), torch.int32)
+        mli = self._moe_index.get(id(lw))
+        ids = self.ws.get("topk_ids" if mli is None else f"topk_ids.{mli}", (T, k), torch.int32)
         wts = self.ws.get("topk_w", (T, k), torch.float32)
         R = T * k
         ex = lw.experts
@@ -320,6 +343,7 @@ class NativeRunner:
             C.moe_route_fused(hb, self._router_w(lw), logits, lw.router_bias, k, cfg.router == "sigmoid",
                               cfg.n_group, cfg.topk_group, cfg.norm_topk_prob, cfg.routed_scaling, ids, wts, MB,
                               rank, stok, posof, pairs, npairs, cnt, self.status)
+            self._ensure_experts(mli, ids)
             y2 = self._moe_gemv_pairs(h2q, h2s, stok, pairs, npairs, ex, R, MB)
         else:
             if T <= 64:
@@ -328,6 +352,7 @@ class NativeRunner:
                 torch.mm(hb.float(), lw.router_w.t(), out=logits)
             C.router_topk(logits, lw.router_bias, k, cfg.router == "sigmoid", cfg.n_group, cfg.topk_group,
                           cfg.norm_topk_prob, cfg.routed_scaling, ids, wts)
+            self._ensure_experts(mli, ids)
             if use_tc:
                 y2, posof = self._moe_tc(h2q, h2s, ids, ex, R, T)
             else:
@@ -554,6 +579,8 @@ class NativeRunner:
 
     def _decode_body(self, st):
         C, k = self.C, self.k
+        if self.cache is not None:
+            self.miss.zero_()      # per-step miss count (read by the replay engine after the step)
         B = st.B
         kp1 = k + 1
         T = B * kp1

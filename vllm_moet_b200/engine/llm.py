@@ -43,7 +43,8 @@ class LLM:
                  num_speculative_tokens: int = 2, max_model_len: int = 4096, max_num_seqs: int = 8,
                  kv_cache_dtype: str = "bf16", seed: int = 0, weights: Optional[ModelWeights] = None,
                  num_layers: Optional[int] = None, cuda_graphs: bool = True, num_gpu_blocks: Optional[int] = None,
-                 tensor_parallel_size: int = 1, tp_group=None, tp_rank: int = 0, **model_overrides):
+                 tensor_parallel_size: int = 1, tp_group=None, tp_rank: int = 0, expert_cache_slots: int = 0,
+                 expert_store: str = "pinned", expert_store_dir: Optional[str] = None, **model_overrides):
         cfg = get_preset(model, **model_overrides) if isinstance(model, str) else model
         if num_layers is not None:
             cfg = cfg.replace(num_layers=num_layers)
@@ -75,6 +76,14 @@ class LLM:
             self.runner = NativeRunner(self.mw, self.ecfg, nb, self.device)
             if tp_group is not None:
                 self.runner.set_tp_group(tp_group)
+            self.cache = self.replay = None
+            slots = expert_cache_slots
+            if not slots and self.ecfg.moet.base_cache_gb > 0:
+                from ..residency import moe_layers
+                sb = moe_layers(self.mw)[0].experts.layout.slot_bytes
+                slots = int(self.ecfg.moet.base_cache_gb * (1 << 30) // sb)
+            if slots:
+                self._attach_cache(slots, expert_store, expert_store_dir, tp_group)
             self._DecodeState = DecodeState
             self._states = {}
             self._pin_active = None
@@ -82,6 +91,23 @@ class LLM:
             from .torch_runner import TorchRunner
             self.blocks = None
             self.runner = TorchRunner(self.mw, self.k, max_model_len, self.device)
+
+    def _attach_cache(self, slots, kind, store_dir, tp_group):
+        """Routed experts from a host store through a GPU expert cache of `slots` slots,
+        with in-graph miss counting and fixed-point replay of missed decode steps."""
+        from ..residency import ReplayEngine, build_expert_cache, checkpoint_id, rank_suffix
+        m = self.ecfg.moet
+        kw = {}
+        if kind in ("pack", "tiered"):
+            kw = dict(dir=store_dir or m.store_dir, ckpt_id=m.ckpt_id or checkpoint_id(cfg=self.cfg, seed=self.ecfg.seed),
+                      suffix=rank_suffix(self.mw.tp_rank, self.mw.tp_size), direct=m.tier_direct,
+                      threads=m.store_threads)
+            if kw["dir"] is None:
+                raise ValueError("pack / tiered expert stores need a store directory (VLLM_MOE_W2_STORE_DIR)")
+        self.cache = build_expert_cache(self.mw, slots, kind, self.device, **kw)
+        self.runner.attach_expert_cache(self.cache)
+        self.replay = ReplayEngine(self.cache, tp_group=tp_group, mode=m.replay_mode, fp_max=m.fp_max,
+                                   miss_tol=m.base_miss_tol)
 
     # ------------------------------------------------------------------ API
     def _normalize(self, prompts) -> List[List[int]]:
@@ -220,7 +246,14 @@ class LLM:
             if self.ecfg.cuda_graphs and graph is None:
                 graph = runner.capture(st)
             t0 = time.perf_counter()
-            if graph is not None:
+            if self.cache is not None:
+                self.cache.wait_idle()           # safe point: no pool / slot-table mutation in flight
+                self.cache.step_begin()
+                snap = st.snapshot()
+                step = graph.replay if graph is not None else (lambda: runner.decode_body(st))
+                self.replay.run(step, lambda: st.restore(snap), lambda: runner.route_ids(B))
+                self.cache.step_end()
+            elif graph is not None:
                 graph.replay()
             else:
                 runner.decode_body(st)

@@ -1,0 +1,240 @@
+"""Per-step control around the expert cache: miss replay, confidence gate,
+speculation guard, routing prefetchers and the pool-size floors.
+
+* :class:`ReplayEngine` -- after a decode step, read the device miss counter;
+  if any routed expert was missing, agree on the missing set across the TP
+  group (MAX of the miss count, union of the per-layer missing bitmaps),
+  fetch it on every rank, agree that every rank succeeded (MIN of an ok
+  flag -- fail closed), restore the step's input state and replay.  Repeats
+  to a fixed point (``strict``: at most ``fp_max`` rounds, then raise;
+  ``approximate``: accept a step with <= ``miss_tol`` misses).  Reference:
+  base-tier replay, patch P:20976-21120 and ``_promote_consensus``.
+* :class:`ConfidenceGate` -- ``max_prob = exp(top1 - logsumexp)`` (or the
+  top1-top2 margin) over the verify rows, aggregated by min or a quantile;
+  at or below ``tau`` the step's routed experts are force-promoted to the
+  higher-precision tier and the step replays (at most ``fp_max`` times).
+  Reference: confidence gate, patch P:9871-10029.
+* :class:`SpecGuard` -- an EMA of the per-step replay indicator; above 0.6
+  it latches draft scheduling off (the cold pool would replay every verify
+  batch), below 0.3 it resumes, and it backs off if suppression does not
+  warm the pool.  Reference: P:8031-8055, ``kpi_step`` P:9565-9626.
+* :class:`LookaheadPrefetcher` -- applies layer L+1's router to layer L's
+  MoE input and queues the predicted experts (LOOKA); :class:`DraftAffinity`
+  folds a token -> experts table from past routing and prefetches the
+  experts of the drafted tokens.  Reference: P:11393-11600.
+* floors: :func:`gate_fire_floor`; :func:`.tier.working_set_floor`.
+"""
+from __future__ import annotations
+
+import collections
+import math
+from typing import Callable, Dict, Iterable, List, Optional, Sequence, Tuple
+
+import torch
+
+from .tier import ExpertCache, FetchError
+
+
+def _tp_reduce(t: torch.Tensor, group, op) -> torch.Tensor:
+    if group is None:
+        return t
+    import torch.distributed as dist
+    dist.all_reduce(t, op=op, group=group)
+    return t
+
+
+class ReplayEngine:
+    def __init__(self, cache: ExpertCache, tp_group=None, mode: str = "strict", fp_max: int = 32,
+                 miss_tol: int = 0, comm_device=None):
+        if mode not in ("strict", "approximate"):
+            raise ValueError(mode)
+        self.cache, self.group, self.mode = cache, tp_group, mode
+        self.fp_max, self.miss_tol = fp_max, miss_tol
+        self.comm_device = comm_device or cache.dev
+        self.stats = collections.Counter()
+
+    def missing_pairs(self, route_ids: Sequence[Optional[torch.Tensor]]) -> List[Tuple[int, int]]:
+        """route_ids[li]: int tensor of routed expert ids of layer li this step (any shape)."""
+        bitmap = torch.zeros(self.cache.L, self.cache.E, dtype=torch.int32)
+        for li, ids in enumerate(route_ids):
+            if ids is None:
+                continue
+            u = torch.unique(ids.detach().reshape(-1).cpu().long())
+            u = u[(u >= 0) & (u < self.cache.E)]
+            bitmap[li, u] = 1
+        bitmap &= (self.cache.mirror < 0).to(torch.int32)
+        if self.group is not None:
+            import torch.distributed as dist
+            bitmap = _tp_reduce(bitmap.to(self.comm_device), self.group, dist.ReduceOp.MAX).cpu()
+        nz = bitmap.nonzero().tolist()
+        return [(int(li), int(e)) for li, e in nz]
+
+    def read_misses(self) -> int:
+        m = self.cache.miss_count.clone()
+        if self.group is not None:
+            import torch.distributed as dist
+            m = _tp_reduce(m.to(self.comm_device), self.group, dist.ReduceOp.MAX)
+        return int(m.item())
+
+    def fetch_consensus(self, pairs) -> None:
+        ok = 1
+        try:
+            self.cache.promote(pairs)
+        except FetchError:
+            ok = 0
+        if self.group is not None:
+            import torch.distributed as dist
+            t = torch.tensor([ok], dtype=torch.int32, device=self.comm_device)
+            ok = int(_tp_reduce(t, self.group, dist.ReduceOp.MIN).item())
+        if not ok:
+            self.stats["fetch_failed"] += 1
+            raise FetchError("expert fetch failed on at least one rank (fail closed)")
+
+    def run(self, step: Callable[[], None], restore: Callable[[], None],
+            route_ids: Callable[[], Sequence[Optional[torch.Tensor]]]) -> int:
+        """Run `step` until it is miss-free.  `restore` puts the step's inputs back
+        before a replay.  -> number of replays."""
+        for it in range(self.fp_max + 1):
+            self.cache.miss_count.zero_()
+            step()
+            misses = self.read_misses()
+            self.stats["steps"] += 1
+            if misses == 0 or (self.mode == "approximate" and misses <= self.miss_tol):
+                self.stats["replays"] += it
+                self.stats["replayed_steps"] += int(it > 0)
+                return it
+            pairs = self.missing_pairs(route_ids())
+            if not pairs:     # counted misses of experts that are resident by now (a concurrent prefetch)
+                pairs = []
+            self.stats["miss_events"] += 1
+            self.fetch_consensus(pairs)
+            restore()
+        if self.mode == "strict":
+            raise RuntimeError(f"expert replay did not converge in {self.fp_max} rounds")
+        return self.fp_max
+
+
+class ConfidenceGate:
+    def __init__(self, tau: float = 0.6, signal: str = "maxprob", agg: str = "min", fp_max: int = 3,
+                 max_promote: int = 64):
+        self.tau, self.signal, self.agg = tau, signal, agg
+        self.fp_max, self.max_promote = fp_max, max_promote
+        self.stats = collections.Counter()
+
+    def score(self, logits: torch.Tensor, rows: Optional[torch.Tensor] = None) -> float:
+        """logits [R, V] (the verify rows).  maxprob = exp(top1 - lse); margin = p1 - p2."""
+        x = logits.float() if rows is None else logits[rows].float()
+        lse = torch.logsumexp(x, dim=-1)
+        if self.signal == "maxprob":
+            s = torch.exp(x.max(dim=-1).values - lse)
+        else:
+            top2 = x.topk(2, dim=-1).values
+            s = torch.exp(top2[:, 0] - lse) - torch.exp(top2[:, 1] - lse)
+        if self.agg == "min":
+            return float(s.min())
+        q = float(self.agg[1:])
+        return float(torch.quantile(s, q))
+
+    def should_fire(self, score: float) -> bool:
+        fire = score <= self.tau
+        self.stats["fired" if fire else "passed"] += 1
+        return fire
+
+    def run(self, step: Callable[[], torch.Tensor], restore: Callable[[], None],
+            routed: Callable[[], List[Tuple[int, int]]], promote: Callable[[List[Tuple[int, int]]], int]) -> int:
+        """step() -> verify logits.  Fires at most fp_max times; promotion failure
+        leaves the step as computed (fail closed: no partial publication)."""
+        n = 0
+        for n in range(self.fp_max + 1):
+            s = self.score(step())
+            if n == self.fp_max or not self.should_fire(s):
+                return n
+            pairs = routed()[: self.max_promote]
+            try:
+                if promote(pairs) == 0:
+                    return n      # nothing left to promote: replay would change nothing
+            except FetchError:
+                self.stats["promote_failed"] += 1
+                return n
+            restore()
+            self.stats["replays"] += 1
+        return n
+
+
+class SpecGuard:
+    def __init__(self, alpha: float = 0.1, hi: float = 0.6, lo: float = 0.3, patience: int = 200):
+        self.alpha, self.hi, self.lo, self.patience = alpha, hi, lo, patience
+        self.ema = 0.0
+        self.suppressed = False
+        self._since = 0
+        self.backoff = 1
+        self._skip = 0
+
+    def observe(self, replayed: bool) -> bool:
+        """Feed one step's replay indicator.  -> whether drafting is allowed next step."""
+        self.ema = (1 - self.alpha) * self.ema + self.alpha * float(replayed)
+        if not self.suppressed and self.ema > self.hi:
+            self.suppressed, self._since = True, 0
+        elif self.suppressed:
+            self._since += 1
+            if self.ema < self.lo:
+                self.suppressed, self.backoff = False, 1
+            elif self._since >= self.patience * self.backoff:
+                # suppression is not warming the pool: resume drafting and back off before latching again
+                self.suppressed, self.backoff, self._since = False, min(self.backoff * 2, 64), 0
+                self.ema = self.lo
+        return not self.suppressed
+
+
+class LookaheadPrefetcher:
+    """Predict layer L+1's experts from layer L's MoE input (routers are cheap)."""
+
+    def __init__(self, cache: ExpertCache, routers: Sequence[torch.Tensor], top_k: int, extra: int = 2):
+        self.cache, self.routers, self.top_k, self.extra = cache, routers, top_k, extra
+        self.stats = collections.Counter()
+
+    def predict(self, li: int, h: torch.Tensor) -> List[Tuple[int, int]]:
+        if li + 1 >= len(self.routers) or self.routers[li + 1] is None:
+            return []
+        logits = h.float() @ self.routers[li + 1].float().t()
+        ids = torch.topk(logits, min(self.top_k + self.extra, logits.shape[-1]), dim=-1).indices
+        return [(li + 1, int(e)) for e in torch.unique(ids).tolist()]
+
+    def step(self, li: int, h: torch.Tensor):
+        pairs = [p for p in self.predict(li, h) if not self.cache.resident(*p)]
+        if pairs:
+            self.stats["requested"] += len(pairs)
+            self.cache.request_prefetch(pairs)
+
+
+class DraftAffinity:
+    """token -> per-layer expert sets learned from routing; prefetch for drafted tokens."""
+
+    def __init__(self, cache: ExpertCache, max_tokens: int = 65536):
+        self.cache = cache
+        self.table: Dict[int, List[set]] = {}
+        self.max_tokens = max_tokens
+
+    def record(self, tokens: Sequence[int], route_ids: Sequence[Optional[torch.Tensor]]):
+        for r, tok in enumerate(tokens):
+            ent = self.table.setdefault(int(tok), [set() for _ in range(self.cache.L)])
+            for li, ids in enumerate(route_ids):
+                if ids is not None and r < ids.shape[0]:
+                    ent[li].update(int(e) for e in ids[r].reshape(-1).tolist())
+        while len(self.table) > self.max_tokens:
+            self.table.pop(next(iter(self.table)))
+
+    def prefetch(self, draft_tokens: Iterable[int]) -> int:
+        pairs = set()
+        for tok in draft_tokens:
+            for li, es in enumerate(self.table.get(int(tok), [])):
+                pairs.update((li, e) for e in es if not self.cache.resident(li, e))
+        if pairs:
+            self.cache.request_prefetch(sorted(pairs))
+        return len(pairs)
+
+
+def gate_fire_floor(moe_layers: int, top_k: int, rows: int, fp_max: int) -> int:
+    """Slots an FP4 gate pool needs: one fire promotes every routed expert of the
+    step, and each replay round can route to new ones (growth 1 + 0.35 (fp_max - 1))."""
+    return int(math.ceil(moe_layers * top_k * rows * (1 + 0.35 * (fp_max - 1))))
