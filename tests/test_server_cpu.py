@@ -1,0 +1,103 @@
+"""OpenAI-compatible server (tiny CPU model) and the DeepSeek-V4 chat encoding."""
+import json
+import socket
+import threading
+import time
+
+import pytest
+import requests
+
+from vllm_moet_b200.entrypoints import chat_encoding as ce
+
+
+def test_effort_normalisation():
+    assert ce.normalize_effort("none") is None
+    assert ce.normalize_effort(None) == "low"
+    assert ce.normalize_effort("xhigh") == "max" and ce.normalize_effort("max") == "max"
+    assert ce.normalize_effort("medium") == "high" and ce.normalize_effort("low") == "low"
+
+
+def test_render_and_parse_roundtrip():
+    tools = [{"type": "function", "function": {"name": "get_weather", "description": "d",
+                                               "parameters": {"type": "object"}}}]
+    msgs = [{"role": "system", "content": "be brief"}, {"role": "user", "content": "weather?"},
+            {"role": "assistant", "content": "", "reasoning_content": "need a tool",
+             "tool_calls": [{"type": "function", "function": {"name": "get_weather",
+                                                               "arguments": '{"city": "Oslo", "days": 3}'}}]},
+            {"role": "tool", "content": "sunny"}]
+    text = ce.render(msgs, tools=tools, reasoning_effort="high")
+    assert text.startswith(ce.BOS + ce.EFFORT_PROMPTS["high"])
+    assert "<tool_result>sunny</tool_result>" in text and "## Tools" in text
+    assert f'<{ce.DSML}parameter name="city" string="true">Oslo</{ce.DSML}parameter>' in text
+    assert f'<{ce.DSML}parameter name="days" string="false">3</{ce.DSML}parameter>' in text
+    assert "need a tool" in text and text.endswith(ce.ASSISTANT + ce.THINK_START)
+    # earlier-turn reasoning is dropped once a later user turn exists
+    t2 = ce.render(msgs + [{"role": "user", "content": "thanks"}], reasoning_effort="low")
+    assert "need a tool" not in t2
+    assert ce.render([{"role": "user", "content": "x"}], reasoning_effort="none").endswith(ce.ASSISTANT + ce.THINK_END)
+    comp = "let me check" + ce.THINK_END + "Sure." + ce.encode_tool_calls(
+        [{"function": {"name": "f", "arguments": {"a": 1, "b": "x"}}}]) + ce.EOS
+    msg = ce.parse_completion(comp, thinking=True)
+    assert msg["reasoning_content"] == "let me check" and msg["content"] == "Sure."
+    assert json.loads(msg["tool_calls"][0]["function"]["arguments"]) == {"a": 1, "b": "x"}
+    with pytest.raises(ValueError):
+        ce.parse_completion("no end of thinking", thinking=True)
+    with pytest.raises(ValueError):
+        ce.parse_completion("a" + ce.THINK_END + "b" + ce.BOS, thinking=True)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.fixture(scope="module")
+def server():
+    import uvicorn
+    from vllm_moet_b200.engine.llm import LLM
+    from vllm_moet_b200.entrypoints.openai_server import EngineWorker, build_app
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+    worker = EngineWorker(llm, "tiny-moe")
+    port = _free_port()
+    srv = uvicorn.Server(uvicorn.Config(build_app(worker), host="127.0.0.1", port=port, log_level="warning"))
+    th = threading.Thread(target=srv.run, daemon=True)
+    th.start()
+    url = f"http://127.0.0.1:{port}"
+    for _ in range(100):
+        try:
+            if requests.get(url + "/health", timeout=1).ok:
+                break
+        except requests.ConnectionError:
+            time.sleep(0.1)
+    yield url, llm
+    srv.should_exit = True
+    th.join(timeout=10)
+    worker.close()
+
+
+def test_completions_match_engine(server):
+    url, llm = server
+    r = requests.post(url + "/v1/completions", json={"prompt": [5, 6, 7, 8], "max_tokens": 6, "ignore_eos": True},
+                      timeout=120)
+    assert r.ok, r.text
+    body = r.json()
+    from vllm_moet_b200.models import reference
+    assert body["choices"][0]["token_ids"] == reference.greedy_generate(llm.mw, [5, 6, 7, 8], 6)
+    assert body["usage"]["completion_tokens"] == 6
+    assert requests.get(url + "/v1/models").json()["data"][0]["id"] == "tiny-moe"
+    assert "moet_requests_total" in requests.get(url + "/metrics").text
+
+
+def test_streaming_and_chat(server):
+    url, _ = server
+    r = requests.post(url + "/v1/completions", json={"prompt": "hi", "max_tokens": 5, "stream": True,
+                                                     "ignore_eos": True}, stream=True, timeout=120)
+    events = [ln[6:] for ln in r.iter_lines(decode_unicode=True) if ln.startswith("data: ")]
+    assert events[-1] == "[DONE]"
+    ids = sum((json.loads(e)["choices"][0]["token_ids"] for e in events[:-1]), [])
+    assert len(ids) == 5 and json.loads(events[-2])["choices"][0]["finish_reason"] == "length"
+    r = requests.post(url + "/v1/chat/completions", json={"messages": [{"role": "user", "content": "hello"}],
+                                                          "max_tokens": 4, "ignore_eos": True}, timeout=120)
+    assert r.ok and r.json()["choices"][0]["message"]["role"] == "assistant"
+    assert requests.post(url + "/v1/completions", json={"prompt": "x", "temperature": 0.7}).status_code == 400

@@ -36,6 +36,7 @@ class _Req:
     t_arrive: float = 0.0
     t_first: float = 0.0
     t_done: float = 0.0
+    callback: Optional[object] = None     # callback(new_token_ids, finish_reason) for streaming
 
 
 class LLM:
@@ -129,7 +130,10 @@ class LLM:
         return out
 
     def generate(self, prompts, sampling_params: Union[SamplingParams, Sequence[SamplingParams], None] = None,
-                 use_tqdm: bool = False) -> List[RequestOutput]:
+                 use_tqdm: bool = False, callbacks: Optional[Sequence] = None) -> List[RequestOutput]:
+        """Greedy generation for a batch of prompts (str, token-id lists or
+        {"prompt_token_ids": [...]}).  `callbacks[i](new_ids, finish_reason)` is
+        called as tokens of prompt i are emitted (streaming)."""
         toks = self._normalize(prompts)
         if sampling_params is None:
             sampling_params = SamplingParams()
@@ -141,7 +145,8 @@ class LLM:
                 raise NotImplementedError("this engine serves greedy decoding (temperature 0) on the MTP path")
             if len(t) + sp.max_tokens + self.k + 1 > self.ecfg.max_model_len:
                 raise ValueError(f"prompt ({len(t)}) + max_tokens ({sp.max_tokens}) exceeds max_model_len")
-            reqs.append(_Req(f"req-{next(self._ids)}", t, sp, t_arrive=time.perf_counter()))
+            reqs.append(_Req(f"req-{next(self._ids)}", t, sp, t_arrive=time.perf_counter(),
+                             callback=callbacks[len(reqs)] if callbacks is not None else None))
         if self.device.type == "cuda":
             self._run_native(reqs)
         else:
@@ -153,16 +158,20 @@ class LLM:
 
     # ------------------------------------------------------------------ helpers
     def _emit(self, r: _Req, tokens) -> bool:
+        n0 = len(r.out)
         for t in tokens:
             if r.finish:
                 break
-            r.out.append(int(t))
-            if not r.params.ignore_eos and (t in r.params.stop_token_ids):
+            t = int(t)
+            r.out.append(t)
+            if not r.params.ignore_eos and (t in r.params.stop_token_ids or t == self.tokenizer.eos_token_id):
                 r.finish = "stop"
             elif len(r.out) >= r.params.max_tokens:
                 r.finish = "length"
         if r.finish and not r.t_done:
             r.t_done = time.perf_counter()
+        if r.callback is not None and (len(r.out) > n0 or r.finish):
+            r.callback(r.out[n0:], r.finish)
         return r.finish is not None
 
     def _run_torch(self, reqs):

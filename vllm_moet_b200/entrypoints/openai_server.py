@@ -1,0 +1,274 @@
+"""OpenAI-compatible HTTP server over the engine.
+
+    python -m vllm_moet_b200.entrypoints.openai_server --model ds4-flash-shape --port 8000
+    torchrun --nproc-per-node 8 -m vllm_moet_b200.entrypoints.openai_server --model ds4-flash-shape
+
+Endpoints: ``GET /health``, ``GET /v1/models``, ``POST /v1/completions``,
+``POST /v1/chat/completions`` (DeepSeek-V4 chat encoding, ``reasoning_effort``,
+tools; ``stream: true`` sends server-sent events ending in ``data: [DONE]``),
+``GET /metrics`` (Prometheus text).
+
+Requests are queued to one engine thread that batches whatever is waiting
+into a single ``LLM.generate`` call (the engine refills finished rows while
+decoding).  Under tensor parallelism rank 0 serves HTTP and broadcasts each
+batch to the other ranks (``torch.distributed.broadcast_object_list``), which
+run the same ``generate`` call in lock step.
+"""
+from __future__ import annotations
+
+import argparse
+import asyncio
+import json
+import os
+import queue
+import threading
+import time
+import uuid
+from typing import Any, Dict, List, Optional
+
+from ..engine.sampling_params import SamplingParams
+from . import chat_encoding
+
+
+class EngineWorker:
+    """Owns the LLM on one thread; requests come in through a queue."""
+
+    def __init__(self, llm, model_name: str, tp_group=None, max_batch: int = 32):
+        self.llm, self.model_name, self.group = llm, model_name, tp_group
+        self.max_batch = max_batch
+        self.q: "queue.Queue" = queue.Queue()
+        self.stats = {"requests": 0, "prompt_tokens": 0, "generated_tokens": 0, "batches": 0}
+        self._stop = False
+        self.thread = threading.Thread(target=self._loop, name="engine", daemon=True)
+        self.thread.start()
+
+    def submit(self, prompt_ids: List[int], params: SamplingParams, on_tokens) -> None:
+        self.q.put((prompt_ids, params, on_tokens))
+
+    def _loop(self):
+        while not self._stop:
+            item = self.q.get()
+            if item is None:
+                break
+            batch = [item]
+            while len(batch) < self.max_batch:
+                try:
+                    nxt = self.q.get_nowait()
+                except queue.Empty:
+                    break
+                if nxt is None:
+                    self._stop = True
+                    break
+                batch.append(nxt)
+            self._run(batch)
+        if self.group is not None:
+            import torch.distributed as dist
+            dist.broadcast_object_list([None], src=0, group=self.group)
+
+    def _run(self, batch):
+        prompts = [b[0] for b in batch]
+        params = [b[1] for b in batch]
+        if self.group is not None:
+            import torch.distributed as dist
+            dist.broadcast_object_list([(prompts, params)], src=0, group=self.group)
+        self.stats["batches"] += 1
+        self.stats["requests"] += len(batch)
+        self.stats["prompt_tokens"] += sum(len(p) for p in prompts)
+        try:
+            outs = self.llm.generate(prompts, params, callbacks=[b[2] for b in batch])
+            self.stats["generated_tokens"] += sum(len(o.outputs[0].token_ids) for o in outs)
+        except Exception as e:  # noqa: BLE001 - report to every waiting request
+            for b in batch:
+                b[2]([], "error:" + str(e))
+
+    def close(self):
+        self.q.put(None)
+        self.thread.join(timeout=10)
+
+
+def follower_loop(llm, tp_group):
+    """Ranks > 0 under TP: run each broadcast batch in lock step with rank 0."""
+    import torch.distributed as dist
+    while True:
+        box = [None]
+        dist.broadcast_object_list(box, src=0, group=tp_group)
+        if box[0] is None:
+            return
+        prompts, params = box[0]
+        llm.generate(prompts, params)
+
+
+def _params_from(body: Dict[str, Any], default_max: int = 16) -> SamplingParams:
+    temp = float(body.get("temperature", 0.0) or 0.0)
+    if temp != 0.0:
+        raise ValueError("only greedy decoding (temperature 0) is served on the MTP path")
+    stop_ids = list(body.get("stop_token_ids") or [])
+    return SamplingParams(max_tokens=int(body.get("max_tokens") or body.get("max_completion_tokens") or default_max),
+                          temperature=0.0, stop_token_ids=stop_ids, ignore_eos=bool(body.get("ignore_eos", False)))
+
+
+def build_app(worker: EngineWorker):
+    from fastapi import FastAPI, HTTPException
+    from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+
+    app = FastAPI(title="vllm_moet_b200 OpenAI-compatible server")
+    tok = worker.llm.tokenizer
+    name = worker.model_name
+
+    def run_request(prompt_ids, params):
+        """-> (asyncio.Queue of (ids, finish)) fed from the engine thread."""
+        loop = asyncio.get_running_loop()
+        aq: "asyncio.Queue" = asyncio.Queue()
+
+        def cb(ids, finish):
+            loop.call_soon_threadsafe(aq.put_nowait, (list(ids), finish))
+        worker.submit(prompt_ids, params, cb)
+        return aq
+
+    async def collect(aq):
+        ids, finish = [], None
+        while finish is None:
+            new, finish = await aq.get()
+            ids += new
+        if finish.startswith("error:"):
+            raise HTTPException(500, finish[6:])
+        return ids, finish
+
+    @app.get("/health")
+    async def health():
+        return {"status": "ok"}
+
+    @app.get("/v1/models")
+    async def models():
+        return {"object": "list", "data": [{"id": name, "object": "model", "owned_by": "vllm_moet_b200",
+                                            "max_model_len": worker.llm.ecfg.max_model_len}]}
+
+    @app.get("/metrics")
+    async def metrics():
+        lines = [f"moet_{k}_total {v}" for k, v in worker.stats.items()]
+        return PlainTextResponse("\n".join(lines) + "\n")
+
+    def _prompt_ids(p):
+        if isinstance(p, str):
+            return [tok.bos_token_id] + tok.encode(p)
+        if isinstance(p, list) and all(isinstance(t, int) for t in p):
+            return list(p)
+        raise HTTPException(400, "prompt must be a string or a list of token ids")
+
+    @app.post("/v1/completions")
+    async def completions(body: Dict[str, Any]):
+        try:
+            params = _params_from(body)
+        except ValueError as e:
+            raise HTTPException(400, str(e))
+        prompts = body.get("prompt")
+        if isinstance(prompts, list) and prompts and not isinstance(prompts[0], int):
+            plist = [_prompt_ids(p) for p in prompts]
+        else:
+            plist = [_prompt_ids(prompts)]
+        rid, created = f"cmpl-{uuid.uuid4().hex[:24]}", int(time.time())
+        if body.get("stream"):
+            if len(plist) != 1:
+                raise HTTPException(400, "streaming serves one prompt per request")
+            aq = run_request(plist[0], params)
+
+            async def gen():
+                finish = None
+                while finish is None:
+                    ids, finish = await aq.get()
+                    if finish and finish.startswith("error:"):
+                        yield f"data: {json.dumps({'error': finish[6:]})}\n\n"
+                        break
+                    chunk = {"id": rid, "object": "text_completion", "created": created, "model": name,
+                             "choices": [{"index": 0, "text": tok.decode(ids), "token_ids": ids,
+                                          "finish_reason": finish}]}
+                    yield f"data: {json.dumps(chunk)}\n\n"
+                yield "data: [DONE]\n\n"
+            return StreamingResponse(gen(), media_type="text/event-stream")
+        qs = [run_request(p, params) for p in plist]
+        choices, n_out = [], 0
+        for i, aq in enumerate(qs):
+            ids, finish = await collect(aq)
+            n_out += len(ids)
+            choices.append({"index": i, "text": tok.decode(ids), "token_ids": ids, "finish_reason": finish,
+                            "logprobs": None})
+        return JSONResponse({"id": rid, "object": "text_completion", "created": created, "model": name,
+                             "choices": choices,
+                             "usage": {"prompt_tokens": sum(map(len, plist)), "completion_tokens": n_out,
+                                       "total_tokens": sum(map(len, plist)) + n_out}})
+
+    @app.post("/v1/chat/completions")
+    async def chat(body: Dict[str, Any]):
+        try:
+            params = _params_from(body)
+        except ValueError as e:
+            raise HTTPException(400, str(e))
+        effort = body.get("reasoning_effort", "none")
+        text = chat_encoding.render(body.get("messages", []), tools=body.get("tools"), reasoning_effort=effort)
+        prompt = [tok.bos_token_id] + tok.encode(text)
+        rid, created = f"chatcmpl-{uuid.uuid4().hex[:24]}", int(time.time())
+        thinking = chat_encoding.normalize_effort(effort) is not None
+        aq = run_request(prompt, params)
+        if body.get("stream"):
+            async def gen():
+                finish = None
+                first = True
+                while finish is None:
+                    ids, finish = await aq.get()
+                    delta = {"content": tok.decode(ids)}
+                    if first:
+                        delta["role"] = "assistant"
+                        first = False
+                    chunk = {"id": rid, "object": "chat.completion.chunk", "created": created, "model": name,
+                             "choices": [{"index": 0, "delta": delta, "finish_reason": finish}]}
+                    yield f"data: {json.dumps(chunk)}\n\n"
+                yield "data: [DONE]\n\n"
+            return StreamingResponse(gen(), media_type="text/event-stream")
+        ids, finish = await collect(aq)
+        out_text = tok.decode(ids)
+        try:
+            msg = chat_encoding.parse_completion(out_text, thinking=thinking)
+        except ValueError:
+            msg = {"role": "assistant", "content": out_text}     # a free-form completion (random-init models)
+        return JSONResponse({"id": rid, "object": "chat.completion", "created": created, "model": name,
+                             "choices": [{"index": 0, "message": msg, "finish_reason": finish}],
+                             "usage": {"prompt_tokens": len(prompt), "completion_tokens": len(ids),
+                                       "total_tokens": len(prompt) + len(ids)}})
+
+    return app
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--model", default="ds4-flash-shape")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--num-layers", type=int, default=None)
+    ap.add_argument("--max-model-len", type=int, default=8192)
+    ap.add_argument("--max-num-seqs", type=int, default=32)
+    ap.add_argument("--num-speculative-tokens", type=int, default=2)
+    ap.add_argument("--device", default=None)
+    args = ap.parse_args(argv)
+    import torch
+    from ..engine.llm import LLM
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl")
+        group = dist.group.WORLD
+    llm = LLM(args.model, device=args.device, num_speculative_tokens=args.num_speculative_tokens,
+              max_model_len=args.max_model_len, max_num_seqs=args.max_num_seqs, num_layers=args.num_layers,
+              tensor_parallel_size=world, tp_group=group, tp_rank=rank)
+    if rank != 0:
+        follower_loop(llm, group)
+        return
+    import uvicorn
+    worker = EngineWorker(llm, args.model, group, max_batch=args.max_num_seqs)
+    uvicorn.run(build_app(worker), host=args.host, port=args.port, log_level="warning")
+
+
+if __name__ == "__main__":
+    main()
