@@ -1,0 +1,66 @@
+"""DSpark width scheduler (the reference's scheduler test semantics), the
+DSpark block drafter, and the greedy / stochastic rejection samplers."""
+import torch
+
+from vllm_moet_b200.spec import DSparkDrafter, allocate_widths, greedy_accept, rejection_sample
+
+
+def test_width_never_exceeds_scheduled_length():
+    w = allocate_widths(torch.ones(2, 4), torch.ones(4), num_reqs=2, length=2, tau=0.5, budget_frac=1.0)
+    assert torch.equal(w, torch.tensor([2, 2], dtype=torch.int32))
+
+
+def test_tied_budget_never_inflates():
+    w = allocate_widths(torch.ones(3, 4), torch.ones(4), num_reqs=3, length=4, tau=0.0, budget_frac=0.25)
+    assert int(w.sum()) == 3 and bool((w <= 4).all())
+
+
+def test_zero_budget_allocates_nothing():
+    w = allocate_widths(torch.rand(2, 4), torch.ones(4), num_reqs=2, length=4, tau=0.0, budget_frac=0.0)
+    assert torch.equal(w, torch.zeros(2, dtype=torch.int32))
+
+
+def test_calibration_projected_to_valid_prefix():
+    w = allocate_widths(torch.tensor([[0.9, 0.8, 0.7, 0.6]]), torch.tensor([1.0, 0.1, 2.0, 2.0]),
+                        num_reqs=1, length=4, tau=0.15, budget_frac=1.0)
+    assert torch.equal(w, torch.tensor([1], dtype=torch.int32))
+
+
+def test_budget_prefers_confident_requests():
+    surv = torch.tensor([[0.9, 0.9, 0.9, 0.9], [0.5, 0.4, 0.3, 0.2]])
+    w = allocate_widths(surv, torch.ones(4), num_reqs=2, length=4, tau=0.1, budget_frac=0.5)
+    assert w.tolist() == [4, 0]
+
+
+def test_greedy_accept_valid_len():
+    tgt = torch.tensor([[5, 6, 7, 8], [5, 6, 7, 8]])
+    dr = torch.tensor([[5, 6, 9], [5, 6, 7]])
+    n, em = greedy_accept(tgt, dr, valid_draft_len=torch.tensor([3, 1]))
+    assert n.tolist() == [2, 1]
+    assert em.tolist() == [[5, 6, 7, -1], [5, 6, -1, -1]]
+
+
+def test_rejection_sampler_preserves_target_distribution():
+    g = torch.Generator().manual_seed(0)
+    V = 4
+    p = torch.tensor([0.1, 0.2, 0.3, 0.4])
+    q = torch.tensor([0.4, 0.3, 0.2, 0.1])
+    N = 20000
+    drafts = torch.multinomial(q.expand(N, V), 1, replacement=True, generator=g)
+    tp = p.expand(N, 2, V).contiguous()
+    dp = q.expand(N, 1, V).contiguous()
+    n, em = rejection_sample(tp, dp, drafts, generator=g)
+    first = em[:, 0]
+    freq = torch.bincount(first, minlength=V).float() / N
+    assert torch.allclose(freq, p, atol=0.015), freq
+
+
+def test_dspark_drafter_shapes():
+    torch.manual_seed(0)
+    d = DSparkDrafter(hidden=32, vocab=50, block=4)
+    drafts, probs, surv = d.propose(torch.randn(3, 32), torch.tensor([1, 2, 3]))
+    assert drafts.shape == (3, 4) and probs.shape == (3, 4, 50)
+    assert bool(((surv > 0) & (surv < 1)).all())
+    assert torch.allclose(probs.sum(-1), torch.ones(3, 4))
+    w = allocate_widths(surv, torch.ones(4), num_reqs=3, length=4, tau=0.0, budget_frac=0.5)
+    assert int(w.sum()) <= 6
