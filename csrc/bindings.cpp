@@ -106,6 +106,9 @@ void ws_gemm_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tens
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_pack_io(m);
+#ifdef MOET_SOURCE_FINGERPRINT
+  m.attr("source_fingerprint") = MOET_SOURCE_FINGERPRINT;
+#endif
   m.doc() = "vllm_moet_b200 sm_100a kernels";
   m.def("rmsnorm_quant", &rmsnorm_quant, py::arg("x"), py::arg("add"), py::arg("x_out"), py::arg("w"), py::arg("eps"),
         py::arg("y_out"), py::arg("q0"), py::arg("s0"), py::arg("q1"), py::arg("s1"), py::arg("ostride"),

@@ -12,6 +12,17 @@ from setuptools import setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def _fingerprint():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("fp", os.path.join(ROOT, "vllm_moet_b200", "ops", "fingerprint.py"))
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    return m.source_fingerprint(ROOT)
+
+
+FP = _fingerprint()
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 sources = sorted(glob.glob(os.path.join("csrc", "*.cpp")) + glob.glob(os.path.join("csrc", "kernels", "*.cu"))
@@ -27,7 +38,7 @@ setup(
             sources=sources,
             include_dirs=[os.path.join(ROOT, "csrc"), os.path.join(ROOT, "csrc", "kernels")],
             extra_compile_args={
-                "cxx": ["-O3", "-std=c++17"],
+                "cxx": ["-O3", "-std=c++17", f'-DMOET_SOURCE_FINGERPRINT="{FP}"'],
                 "nvcc": ARCH + ["-O3", "-std=c++17", "-lineinfo", "--use_fast_math",
                                 "-Xptxas", "-warn-spills",
                                 "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_BFLOAT16_CONVERSIONS__"],

@@ -1,0 +1,160 @@
+"""Recipe runner, result lint and renderer (see the package docstring)."""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import subprocess
+import sys
+import time
+from typing import List
+
+import torch
+import yaml
+
+SCHEMA = 2
+RECIPE_DIR = os.path.join(os.path.dirname(__file__), "recipes")
+REQUIRED = ("schema", "recipe", "recipe_sha256", "git_commit", "source_fingerprint", "device", "results", "time")
+
+
+def resolve_recipe(arg: str) -> str:
+    if os.path.exists(arg):
+        return arg
+    p = os.path.join(RECIPE_DIR, arg if arg.endswith(".yaml") else arg + ".yaml")
+    if not os.path.exists(p):
+        raise FileNotFoundError(f"no recipe {arg!r} (have {sorted(os.listdir(RECIPE_DIR))})")
+    return p
+
+
+def file_sha(path: str) -> str:
+    with open(path, "rb") as f:
+        return hashlib.sha256(f.read()).hexdigest()
+
+
+def git_commit() -> str:
+    try:
+        return subprocess.run(["git", "rev-parse", "HEAD"], capture_output=True, text=True, timeout=10,
+                              cwd=os.path.dirname(os.path.abspath(__file__))).stdout.strip() or "unknown"
+    except (OSError, subprocess.SubprocessError):
+        return "unknown"
+
+
+def _sync(dev):
+    if dev.type == "cuda":
+        torch.cuda.synchronize()
+
+
+def run_recipe(path: str) -> dict:
+    from ..engine.llm import LLM
+    from ..engine.sampling_params import SamplingParams
+    from ..ops.fingerprint import source_fingerprint
+    with open(path) as f:
+        rec = yaml.safe_load(f)
+    eng = dict(rec.get("engine", {}))
+    llm = LLM(rec["model"], **eng, **rec.get("overrides", {}))
+    g = torch.Generator().manual_seed(0)
+    V = llm.cfg.vocab
+
+    def prompt(n):
+        return torch.randint(3, V, (n,), generator=g).tolist()
+    results: List[dict] = []
+    for pr in rec.get("probes", []):
+        kind = pr["kind"]
+        if kind == "decode":
+            for S in pr["streams"]:
+                ps = [prompt(pr["prompt_len"]) for _ in range(S)]
+                sp = SamplingParams(max_tokens=pr["tokens"], ignore_eos=True)
+                llm.generate(ps, SamplingParams(max_tokens=2, ignore_eos=True))
+                outs = llm.generate(ps, sp)
+                st = llm.stats
+                gen = sum(len(o.outputs[0].token_ids) - 1 for o in outs)
+                secs = st.get("decode_s") or 1e-9
+                results.append({"probe": "decode", "streams": S, "tok_s": gen / secs if "decode_s" in st else None,
+                                "steps": st.get("steps"), "accepted": st.get("accepted")})
+        elif kind == "prefill":
+            for n in pr["lengths"]:
+                p = prompt(n)
+                llm.generate([p], SamplingParams(max_tokens=1, ignore_eos=True))
+                t0 = time.perf_counter()
+                llm.generate([p], SamplingParams(max_tokens=1, ignore_eos=True))
+                _sync(llm.device)
+                dt = time.perf_counter() - t0
+                results.append({"probe": "prefill", "length": n, "tok_s": n / dt, "ms": dt * 1e3})
+        elif kind == "coherence":
+            p = prompt(pr["prompt_len"])
+            sp = SamplingParams(max_tokens=pr["tokens"], ignore_eos=True)
+            a = llm.generate([p], sp)[0].outputs[0].token_ids
+            b = llm.generate([p], sp)[0].outputs[0].token_ids
+            results.append({"probe": "coherence", "identical": a == b, "tokens": len(a)})
+        else:
+            raise ValueError(f"unknown probe kind {kind!r}")
+    dev = torch.cuda.get_device_name(0) if torch.cuda.is_available() and llm.device.type == "cuda" else "cpu"
+    return {"schema": SCHEMA, "recipe": rec["name"], "recipe_sha256": file_sha(path), "git_commit": git_commit(),
+            "source_fingerprint": source_fingerprint(), "device": dev, "results": results,
+            "time": time.strftime("%Y-%m-%dT%H:%M:%SZ", time.gmtime())}
+
+
+def lint(result: dict, recipe_path: str = None) -> List[str]:
+    errs = [f"missing field {k}" for k in REQUIRED if k not in result]
+    if result.get("schema") != SCHEMA:
+        errs.append(f"schema {result.get('schema')} != {SCHEMA}")
+    if recipe_path is None and "recipe" in result:
+        try:
+            recipe_path = resolve_recipe(result["recipe"])
+        except FileNotFoundError:
+            errs.append(f"recipe {result['recipe']} not found")
+    if recipe_path and "recipe_sha256" in result and file_sha(recipe_path) != result["recipe_sha256"]:
+        errs.append("recipe changed since the result was produced (sha256 mismatch)")
+    for r in result.get("results", []):
+        if "probe" not in r:
+            errs.append("a result row without a probe kind")
+    return errs
+
+
+def render(results: List[dict]) -> str:
+    rows = ["| recipe | device | probe | setting | value |", "|---|---|---|---|---|"]
+    for res in results:
+        for r in res["results"]:
+            if r["probe"] == "decode":
+                rows.append(f"| {res['recipe']} | {res['device']} | decode | {r['streams']} streams | "
+                            f"{(r['tok_s'] or 0):.1f} tok/s |")
+            elif r["probe"] == "prefill":
+                rows.append(f"| {res['recipe']} | {res['device']} | prefill | {r['length']} tokens | "
+                            f"{r['tok_s']:.0f} tok/s |")
+            else:
+                rows.append(f"| {res['recipe']} | {res['device']} | coherence | {r['tokens']} tokens | "
+                            f"{'identical' if r['identical'] else 'DIFFERENT'} |")
+    return "\n".join(rows)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(prog="python -m vllm_moet_b200.bench")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    r = sub.add_parser("run"); r.add_argument("recipe"); r.add_argument("--out", default="bench_results")
+    li = sub.add_parser("lint"); li.add_argument("files", nargs="+")
+    rn = sub.add_parser("render"); rn.add_argument("files", nargs="+")
+    a = ap.parse_args(argv)
+    if a.cmd == "run":
+        path = resolve_recipe(a.recipe)
+        res = run_recipe(path)
+        os.makedirs(a.out, exist_ok=True)
+        out = os.path.join(a.out, f"{res['recipe']}.{int(time.time())}.json")
+        with open(out, "w") as f:
+            json.dump(res, f, indent=1)
+        print(out)
+    elif a.cmd == "lint":
+        bad = 0
+        for fn in a.files:
+            with open(fn) as f:
+                errs = lint(json.load(f))
+            for e in errs:
+                print(f"{fn}: {e}")
+            bad += bool(errs)
+        sys.exit(1 if bad else 0)
+    else:
+        res = []
+        for fn in a.files:
+            with open(fn) as f:
+                res.append(json.load(f))
+        print(render(res))

@@ -105,6 +105,8 @@ class LLM:
                       threads=m.store_threads)
             if kw["dir"] is None:
                 raise ValueError("pack / tiered expert stores need a store directory (VLLM_MOE_W2_STORE_DIR)")
+        from ..utils.observability import KpiLogger
+        self.kpi = KpiLogger(every=m.kpi_every)
         self.cache = build_expert_cache(self.mw, slots, kind, self.device, **kw)
         self.runner.attach_expert_cache(self.cache)
         self.replay = ReplayEngine(self.cache, tp_group=tp_group, mode=m.replay_mode, fp_max=m.fp_max,
@@ -260,8 +262,11 @@ class LLM:
                 self.cache.step_begin()
                 snap = st.snapshot()
                 step = graph.replay if graph is not None else (lambda: runner.decode_body(st))
-                self.replay.run(step, lambda: st.restore(snap), lambda: runner.route_ids(B))
+                f0 = self.cache.stats["fetched_rows"]
+                n_rep = self.replay.run(step, lambda: st.restore(snap), lambda: runner.route_ids(B))
                 self.cache.step_end()
+                self.kpi.step(replayed=n_rep > 0, misses=self.cache.stats["fetched_rows"] - f0,
+                              fetched_rows=self.cache.stats["fetched_rows"] - f0)
             elif graph is not None:
                 graph.replay()
             else:

@@ -21,7 +21,10 @@ def native():
     if _C is not None:
         return _C
     try:
-        _C = importlib.import_module("vllm_moet_b200._C")
+        mod = importlib.import_module("vllm_moet_b200._C")
+        from .fingerprint import check_build
+        check_build(mod)
+        _C = mod
     except ImportError as e:  # pragma: no cover - depends on the build
         _err = e
         raise RuntimeError(
