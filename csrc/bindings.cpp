@@ -47,6 +47,9 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
 void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::optional<torch::Tensor> resid,
                  c10::optional<torch::Tensor> shared_out, c10::optional<torch::Tensor> out,
                  c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> ar);
+// bf12.cu
+void bf12_decode(torch::Tensor cls, torch::Tensor lo, torch::Tensor lut, torch::Tensor esc_pos, torch::Tensor esc_hi,
+                 torch::Tensor out);
 // symm.cu
 std::tuple<int64_t, at::Tensor> symm_alloc(int64_t bytes);
 int64_t symm_open(at::Tensor handle);
@@ -135,6 +138,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_w2_gemv", &moe_w2_gemv);
   m.def("moe_combine", &moe_combine, py::arg("y"), py::arg("pos_of"), py::arg("wts"), py::arg("resid"),
         py::arg("shared_out"), py::arg("out"), py::arg("out_f32"), py::arg("ar") = py::none());
+  m.def("bf12_decode", &bf12_decode);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);
