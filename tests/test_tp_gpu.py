@@ -48,7 +48,7 @@ def _tp_engine(rank, world, fused):
     from vllm_moet_b200 import SamplingParams
     from vllm_moet_b200.engine.llm import LLM
     from vllm_moet_b200.models import reference
-    os.environ["MOET_TP_FUSED"] = "1" if fused else "0"
+    os.environ["MOET_TP_FUSED"] = "1" if fused else "0"     # read by set_tp_group
     cfg = _small_cfg()
     llm = LLM(cfg, device="cuda", num_speculative_tokens=2, max_model_len=512, max_num_seqs=2,
               tensor_parallel_size=world, tp_group=dist.group.WORLD, tp_rank=rank)
@@ -76,3 +76,27 @@ def test_tp2_engine_tracks_oracle(fused):
     assert o0 == o1                      # both ranks emit the same tokens
     assert all(len(o) == 10 for o in o0)
     assert max(w0, w1) < 0.5, (w0, w1)   # each token is the oracle argmax or a near-tie
+
+
+def _pp_engine(rank, world):
+    import torch.distributed as dist
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    cfg = _small_cfg()
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(3, 2048, (n,), generator=g).tolist() for n in (33, 70)]
+    sp = SamplingParams(max_tokens=10, ignore_eos=True)
+    llm = LLM(cfg, device="cuda", num_speculative_tokens=2, max_model_len=512, max_num_seqs=2,
+              pipeline_parallel_size=world, pp_group=dist.group.WORLD, pp_rank=rank)
+    outs = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
+    ref = None
+    if rank == 0:     # the same model on one GPU (per-layer weight streams make it identical)
+        one = LLM(cfg, device="cuda", num_speculative_tokens=2, max_model_len=512, max_num_seqs=2, cuda_graphs=False)
+        ref = [o.outputs[0].token_ids for o in one.generate(prompts, sp)]
+    return outs, ref
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_pp2_matches_single_gpu():
+    (o0, ref), (o1, _) = run_ranks(_pp_engine, 2, backend="nccl", env={"NCCL_NVLS_ENABLE": "0"})
+    assert o0 == o1 == ref

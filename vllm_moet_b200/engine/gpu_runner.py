@@ -83,7 +83,8 @@ class NativeRunner:
         self.cfg: ModelConfig = mw.cfg
         self.ecfg = ecfg
         self.dev = torch.device(device)
-        self.k = ecfg.num_speculative_tokens if mw.mtp is not None else 0
+        has_mtp = mw.mtp is not None or (mw.extra.get("pp_size", 1) > 1 and mw.cfg.num_mtp_layers > 0)
+        self.k = ecfg.num_speculative_tokens if has_mtp else 0
         self.Hh = self.cfg.num_heads // mw.tp_size
         cfg = self.cfg
         self.num_blocks = num_blocks
@@ -108,6 +109,10 @@ class NativeRunner:
         self._moe_index = {}
         self._pend = None         # (residual, out) of a pushed reduction the next RMSNorm completes
         self._fused = False
+        # pipeline parallelism: this stage's layers; first stage embeds, last stage owns head + MTP
+        self.pp_group = None
+        self.pp_rank, self.pp_size = mw.extra.get("pp_rank", 0), mw.extra.get("pp_size", 1)
+        self.first_stage, self.last_stage = self.pp_rank == 0, self.pp_rank == self.pp_size - 1
         self.nsplit = 8
         self._side = torch.cuda.Stream(device=self.dev)   # second graph branch for independent chains
         import os
@@ -178,12 +183,13 @@ class NativeRunner:
     def set_tp_group(self, group, fused: Optional[bool] = None):
         """Join a tensor-parallel group.  Decode-sized reductions then run fused
         over peer memory (producer epilogues push, the next RMSNorm reduces);
-        prefill-sized ones use NCCL all-reduce.  MOET_TP_FUSED=0 selects NCCL
-        everywhere (the baseline)."""
+        prefill-sized ones use NCCL all-reduce.  MOET_TP_FUSED=1 enables the
+        fused path (default off: at TP2 on the DS4 shape it measured 6.93 ms per
+        decode step against 6.52 ms for NCCL all-reduce)."""
         import os
         self.tp_group = group
         if fused is None:
-            fused = os.environ.get("MOET_TP_FUSED", "1") != "0"
+            fused = os.environ.get("MOET_TP_FUSED", "0") == "1"
         if fused and group is not None:
             from ..parallel.symm import SymmAllReduce
             self.ar = SymmAllReduce(group, 128 * self.cfg.hidden, self.dev, self.status)
@@ -207,6 +213,34 @@ class NativeRunner:
         if self.cache is None or li is None or torch.cuda.is_current_stream_capturing():
             return
         self.cache.ensure_resident(li, torch.unique(ids).tolist())
+
+    def set_pp_group(self, group):
+        """Join a pipeline group: stage activations travel by NCCL send/recv and
+        the last stage broadcasts each step's accepted tokens, drafts and
+        positions to every stage."""
+        self.pp_group = group
+
+    def _pp_peer(self, r):
+        return torch.distributed.get_global_rank(self.pp_group, r)
+
+    def _pp_broadcast_state(self, st, rows=None):
+        """Last stage -> all stages: the decode state every stage needs for the next step."""
+        if self.pp_group is None or self.pp_size == 1:
+            return
+        src = self._pp_peer(self.pp_size - 1)
+        for t in (st.tokens, st.seq_pos, st.out_tokens, st.n_acc):
+            torch.distributed.broadcast(t, src=src, group=self.pp_group)
+
+    def _materialize(self, x):
+        """Complete a pending fused all-reduce into x (no norm outputs)."""
+        if self._pend is not None:
+            resid, xout = self._pend
+            self._pend = None
+            ones = self.ws.get("pp.ones", (self.cfg.hidden,), torch.bfloat16)
+            ones.fill_(1.0)
+            self.C.rmsnorm_quant(resid, None, xout, ones, self.cfg.rms_eps, None, None, None, None, None, 0,
+                                 self.ar.desc)
+        return x
 
     def _tp_allreduce(self, t):
         if self.tp_group is not None:
@@ -452,12 +486,17 @@ class NativeRunner:
 
     # ------------------------------------------------------------------ model pieces
     def _main(self, tokens, ctx: StepCtx):
-        x = torch.nn.functional.embedding(tokens.long(), self.mw.embed)
         xin = self.ws.get("x_in", (ctx.T, self.cfg.hidden), torch.bfloat16)
-        xin.copy_(x)
+        if self.first_stage:
+            xin.copy_(torch.nn.functional.embedding(tokens.long(), self.mw.embed))
+        else:       # activations of the previous pipeline stage
+            torch.distributed.recv(xin, src=self._pp_peer(self.pp_rank - 1), group=self.pp_group)
         x = xin
         for li, lw in enumerate(self.mw.layers):
             x = self._layer(lw, x, ctx, self.kv[li], li)
+        if not self.last_stage:
+            x = self._materialize(x)
+            torch.distributed.send(x.contiguous(), dst=self._pp_peer(self.pp_rank + 1), group=self.pp_group)
         return x
 
     def _final(self, x, rows, tag):
@@ -476,7 +515,8 @@ class NativeRunner:
         """MTP module over rows (h_i, token_{i+1}) -> (head-normed hidden, logits)."""
         cfg, C, m = self.cfg, self.C, self.mw.mtp
         T, H = ctx.T, cfg.hidden
-        emb = torch.nn.functional.embedding(next_tokens.long(), self.mw.embed)
+        table = self.mw.embed if self.mw.embed is not None else self.mw.extra["mtp_embed"]
+        emb = torch.nn.functional.embedding(next_tokens.long(), table)
         ehq, ehs = self._fp8("eh", T, 2 * H)
         C.rmsnorm_quant(emb, None, None, m.enorm, cfg.rms_eps, None, ehq, ehs, None, None, 2 * H)
         C.rmsnorm_quant(hidden, None, None, m.hnorm, cfg.rms_eps, None, ehq[:, H:], ehs[:, H // 64:], None, None,
@@ -523,14 +563,21 @@ class NativeRunner:
         ctx = StepCtx(T=T, pos=pos, seq=seq, slot=slot, block_table=bt, mode="prefill", cu_seqlens=cu,
                       max_len=max(lens), mb=32)
         x = self._main(toks, ctx)
+        B = len(prompts)
+        if not self.last_stage:     # the last stage computes the first tokens and drafts, then broadcasts them
+            cur = torch.tensor(lens, dtype=torch.int32, device=dev)
+            state.set_rows(seq_rows, torch.zeros(B, dtype=torch.int32, device=dev), cur,
+                           torch.zeros(B, max(self.k, 1), dtype=torch.int32, device=dev)[:, :self.k] if self.k else None)
+            self._pp_broadcast_state(state)
+            return state.tokens[torch.tensor(seq_rows, device=dev), 0].clone()
         last = (cu[1:] - 1).long()
         xl = x[last].contiguous()
         hid_last, logits = self._final(xl, None, "main")
         tgt = self.ws.get("pf.tgt", (len(prompts),), torch.int32)
         self._argmax(logits, tgt)
-        B = len(prompts)
         if self.k == 0:
             state.set_rows(seq_rows, tgt, torch.tensor(lens, dtype=torch.int32, device=dev), None)
+            self._pp_broadcast_state(state)
             return tgt
         # full hidden for the MTP pass: final norm over all rows
         hid_all = self.ws.get("pf.hid", (T, self.cfg.hidden), torch.bfloat16)
@@ -557,6 +604,7 @@ class NativeRunner:
             drafts[:, j] = dj
             prev_tok = dj.clone()
         state.set_rows(seq_rows, tgt, cur_pos, drafts)
+        self._pp_broadcast_state(state)
         return tgt
 
     # ------------------------------------------------------------------ decode
@@ -591,12 +639,16 @@ class NativeRunner:
         ctx = StepCtx(T=T, pos=pos.int(), seq=st.seq_rows, slot=slot, block_table=st.block_table, mode="decode",
                       mb=8 if T * self.cfg.top_k <= 256 else 16)
         x = self._main(st.tokens.view(-1), ctx)
+        if not self.last_stage:
+            self._pp_broadcast_state(st)
+            return
         hid, logits = self._final(x, None, "main")
         self._argmax(logits, st.targets.view(-1))
         C.mtp_accept(st.targets, st.tokens, st.out_tokens, st.n_acc, st.active)
         if k == 0:
             st.seq_pos.add_(st.active)
             st.tokens.copy_(st.targets)
+            self._pp_broadcast_state(st)
             return
         # MTP pass 1 over the verify rows: (h_j, target_j) at position p + j
         mh, mlog = self._mtp(hid, st.targets.view(-1), ctx)
@@ -619,6 +671,7 @@ class NativeRunner:
             st.drafts[:, j] = dj
             prev_tok = dj
         C.mtp_finalize(st.targets, st.n_acc, st.drafts, st.tokens, st.seq_pos, st.active)
+        self._pp_broadcast_state(st)
 
     def capture(self, st, warm: bool = True):
         """Capture decode_body for the state's batch bucket (after one eager warm-up)."""

@@ -44,7 +44,8 @@ class LLM:
                  num_speculative_tokens: int = 2, max_model_len: int = 4096, max_num_seqs: int = 8,
                  kv_cache_dtype: str = "bf16", seed: int = 0, weights: Optional[ModelWeights] = None,
                  num_layers: Optional[int] = None, cuda_graphs: bool = True, num_gpu_blocks: Optional[int] = None,
-                 tensor_parallel_size: int = 1, tp_group=None, tp_rank: int = 0, expert_cache_slots: int = 0,
+                 tensor_parallel_size: int = 1, tp_group=None, tp_rank: int = 0,
+                 pipeline_parallel_size: int = 1, pp_group=None, pp_rank: int = 0, expert_cache_slots: int = 0,
                  expert_store: str = "pinned", expert_store_dir: Optional[str] = None, **model_overrides):
         cfg = get_preset(model, **model_overrides) if isinstance(model, str) else model
         if num_layers is not None:
@@ -58,15 +59,20 @@ class LLM:
             cfg = cfg.replace(dense_dtype="fp8")
         self.cfg = cfg
         self.ecfg = EngineConfig(model=cfg, moet=MoetConfig.from_env(),
-                                 parallel=ParallelConfig(tp=tensor_parallel_size),
+                                 parallel=ParallelConfig(tp=tensor_parallel_size, pp=pipeline_parallel_size),
                                  max_num_seqs=max_num_seqs, max_model_len=max_model_len,
                                  kv_cache_dtype=kv_cache_dtype, num_speculative_tokens=num_speculative_tokens,
                                  cuda_graphs=cuda_graphs, seed=seed, device=str(self.device))
         self.tokenizer = ByteTokenizer(cfg.vocab)
         self.mw = weights if weights is not None else random_weights(
             cfg, self.device, seed=seed, tp_rank=tp_rank, tp_size=tensor_parallel_size,
-            with_mtp=num_speculative_tokens > 0)
-        self.k = num_speculative_tokens if self.mw.mtp is not None else 0
+            with_mtp=num_speculative_tokens > 0, pp_rank=pp_rank, pp_size=pipeline_parallel_size)
+        if pipeline_parallel_size > 1:
+            # MTP presence is a property of the model, known on every stage
+            self._has_mtp = num_speculative_tokens > 0 and cfg.num_mtp_layers > 0
+        else:
+            self._has_mtp = self.mw.mtp is not None
+        self.k = num_speculative_tokens if self._has_mtp else 0
         self.max_blocks = -(-(max_model_len + self.k + 2) // 64)
         self.stats = {}
         self._ids = itertools.count()
@@ -77,6 +83,9 @@ class LLM:
             self.runner = NativeRunner(self.mw, self.ecfg, nb, self.device)
             if tp_group is not None:
                 self.runner.set_tp_group(tp_group)
+            if pp_group is not None:
+                self.runner.set_pp_group(pp_group)
+                self.ecfg.cuda_graphs = False      # pipeline stages run eager steps (p2p per step)
             self.cache = self.replay = None
             slots = expert_cache_slots
             if not slots and self.ecfg.moet.base_cache_gb > 0:

@@ -300,7 +300,8 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
       * routed experts: every expert's intermediate dimension split (w13 rows,
         w2 columns), so each rank streams 1/tp of every routed expert."""
     H, dt = cfg.hidden, cfg.dense_dtype
-    nh = cfg.num_heads
+    rng.counter = 1000 * (li + 1)      # per-layer draw stream: a layer's weights do not depend on which
+    nh = cfg.num_heads                 # other layers a (pipeline) stage builds
     assert nh % tp_size == 0, "num_heads must divide by the TP size"
     Hh = nh // tp_size
     qk = cfg.qk_head_dim
@@ -384,24 +385,47 @@ def _vocab_shard(w: torch.Tensor, tp_rank: int, tp_size: int) -> torch.Tensor:
     return w[tp_rank * per:(tp_rank + 1) * per].contiguous()
 
 
+def pp_layer_range(num_layers: int, pp_rank: int, pp_size: int):
+    """Contiguous, balanced layer range of a pipeline stage."""
+    per, extra = divmod(num_layers, pp_size)
+    l0 = pp_rank * per + min(pp_rank, extra)
+    return l0, l0 + per + (1 if pp_rank < extra else 0)
+
+
 def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int = 0, tp_size: int = 1,
-                   with_mtp: bool = True, num_layers: Optional[int] = None) -> ModelWeights:
-    """Synthetic random-init weights of the given architecture (N(0, 0.02))."""
+                   with_mtp: bool = True, num_layers: Optional[int] = None, pp_rank: int = 0,
+                   pp_size: int = 1) -> ModelWeights:
+    """Synthetic random-init weights of the given architecture (N(0, 0.02)).
+    With pp_size > 1 only the stage's layers are built; the first stage holds
+    the embedding, the last the final norm, the head and the MTP module."""
     dev = torch.device(device)
     rng = _Rng(seed, dev)
     H = cfg.hidden
     L = cfg.num_layers if num_layers is None else num_layers
-    embed = rng.normal((cfg.vocab, H)).to(torch.bfloat16)
-    layers = [_make_layer(cfg, rng, i, dev, cfg.is_moe_layer(i), tp_rank, tp_size) for i in range(L)]
+    l0, l1 = pp_layer_range(L, pp_rank, pp_size)
+    first, last = pp_rank == 0, pp_rank == pp_size - 1
+    rng.counter = 0
+    embed = rng.normal((cfg.vocab, H)).to(torch.bfloat16) if first else None
+    layers = [_make_layer(cfg, rng, i, dev, cfg.is_moe_layer(i), tp_rank, tp_size) for i in range(l0, l1)]
+    head = None
+    if last:
+        rng.counter = 1
+        head = make_linear(_vocab_shard(rng.normal((cfg.vocab, H)), tp_rank, tp_size), cfg.dense_dtype)
     mw = ModelWeights(cfg=cfg, embed=embed, layers=layers,
                       final_norm=torch.ones(H, dtype=torch.bfloat16, device=dev),
-                      lm_head=make_linear(_vocab_shard(rng.normal((cfg.vocab, H)), tp_rank, tp_size), cfg.dense_dtype),
-                      tp_rank=tp_rank, tp_size=tp_size)
-    if with_mtp and cfg.num_mtp_layers:
+                      lm_head=head, tp_rank=tp_rank, tp_size=tp_size)
+    mw.extra.update(layer_range=(l0, l1), pp_rank=pp_rank, pp_size=pp_size)
+    if with_mtp and cfg.num_mtp_layers and last:
+        rng.counter = 2
+        eh = make_linear(rng.normal((H, 2 * H)), cfg.dense_dtype)
+        # the MTP module shares the head; its embedding copy lives on the last stage
+        if mw.embed is None:
+            rng.counter = 0
+            mw.extra["mtp_embed"] = rng.normal((cfg.vocab, H)).to(torch.bfloat16)
         mw.mtp = MTPWeights(
             enorm=torch.ones(H, dtype=torch.bfloat16, device=dev),
             hnorm=torch.ones(H, dtype=torch.bfloat16, device=dev),
-            eh_proj=make_linear(rng.normal((H, 2 * H)), cfg.dense_dtype),
+            eh_proj=eh,
             layer=_make_layer(cfg, rng, L, dev, True, tp_rank, tp_size),
             head_norm=torch.ones(H, dtype=torch.bfloat16, device=dev))
     return mw
