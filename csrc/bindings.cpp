@@ -47,6 +47,10 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
 void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::optional<torch::Tensor> resid,
                  c10::optional<torch::Tensor> shared_out, c10::optional<torch::Tensor> out,
                  c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> ar);
+// indexer.cu
+void indexer_logits(torch::Tensor q, torch::Tensor w, torch::Tensor k_cache, torch::Tensor block_table,
+                    torch::Tensor seq_of_tok, torch::Tensor pos_of_tok, torch::Tensor out, torch::Tensor status);
+void indexer_topk(torch::Tensor scores, int64_t k, torch::Tensor out);
 // bf12.cu
 void bf12_decode(torch::Tensor cls, torch::Tensor lo, torch::Tensor lut, torch::Tensor esc_pos, torch::Tensor esc_hi,
                  torch::Tensor out);
@@ -61,7 +65,7 @@ void ar_test(at::Tensor desc, at::Tensor x, c10::optional<at::Tensor> resid, at:
 // mla_decode.cu
 void mla_decode(torch::Tensor q, torch::Tensor kv, torch::Tensor block_table, torch::Tensor seq_of_tok,
                 torch::Tensor pos_of_tok, torch::Tensor o_part, torch::Tensor ml_part, double scale,
-                torch::Tensor status);
+                torch::Tensor status, c10::optional<torch::Tensor> sel);
 void mla_combine(torch::Tensor o_part, torch::Tensor ml_part, c10::optional<torch::Tensor> out,
                  c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> qs);
 // mla_prep.cu
@@ -139,13 +143,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine, py::arg("y"), py::arg("pos_of"), py::arg("wts"), py::arg("resid"),
         py::arg("shared_out"), py::arg("out"), py::arg("out_f32"), py::arg("ar") = py::none());
   m.def("bf12_decode", &bf12_decode);
+  m.def("indexer_logits", &indexer_logits);
+  m.def("indexer_topk", &indexer_topk);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);
   m.def("symm_free", &symm_free);
   m.def("symm_view", &symm_view);
   m.def("ar_test", &ar_test);
-  m.def("mla_decode", &mla_decode);
+  m.def("mla_decode", &mla_decode, py::arg("q"), py::arg("kv"), py::arg("block_table"), py::arg("seq_of_tok"),
+        py::arg("pos_of_tok"), py::arg("o_part"), py::arg("ml_part"), py::arg("scale"), py::arg("status"),
+        py::arg("sel") = py::none());
   m.def("mla_combine", &mla_combine);
   m.def("q_prep", &q_prep);
   m.def("kv_prep", &kv_prep);

@@ -25,6 +25,12 @@ constexpr int kRow = 584;         // bf16 elements per cache row
 constexpr int kLat = 512, kQK = 576;
 constexpr int kBlockBytes = kBS * kRow * 2;
 constexpr int kPRow = 72;         // P smem row (bf16), 144 B stride
+constexpr int kRow4 = 352;        // NVFP4 cache row bytes: 256 e2m1 | 32 e4m3 scales | 64 e4m3 rope
+constexpr int kBlockBytes4 = kBS * kRow4;
+
+// e2m1 code -> value (sign in bit 3)
+__device__ __constant__ float kE2M1[16] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f,
+                                           -0.f, -0.5f, -1.f, -1.5f, -2.f, -3.f, -4.f, -6.f};
 
 MOET_DEVICE uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 MOET_DEVICE void mbar_init(uint64_t* bar, int count) {
@@ -63,14 +69,59 @@ struct MlaDecodeArgs {
   int T, Hh, nsplit;
   float scale_log2;                                    // softmax scale * log2(e)
   int* status;
+  int nvfp4;                                           // cache rows are 352-byte NVFP4 (kv: uint8 [blocks, 64, 352])
+  const int* sel; int sel_stride;                      // sparse mode: [T, topk] selected positions (-1 = none)
 };
+
+// Expand one staged NVFP4 block (64 rows x 352 B) into the bf16 tile [64][584]:
+// latent = e2m1 * e4m3(block-16 scale) * 2^-6, rope = e4m3.
+MOET_DEVICE void expand_nvfp4_block(const uint8_t* __restrict__ st, __nv_bfloat16* __restrict__ kvt) {
+  for (int task = threadIdx.x; task < kBS * 16; task += blockDim.x) {
+    const int r = task >> 4, c = task & 15;              // 16-byte chunk c = 32 latent dims
+    const uint8_t* row = st + r * kRow4;
+    const uint4 b = *reinterpret_cast<const uint4*>(row + c * 16);
+    const float s0 = e4m3_to_f32(row[256 + 2 * c]) * 0.015625f, s1 = e4m3_to_f32(row[256 + 2 * c + 1]) * 0.015625f;
+    const uint32_t w[4] = {b.x, b.y, b.z, b.w};
+    uint32_t o[16];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const uint32_t byte = (w[i] >> (8 * j)) & 0xFF;
+        const float sc = i < 2 ? s0 : s1;
+        const __nv_bfloat162 v = __floats2bfloat162_rn(kE2M1[byte & 0xF] * sc, kE2M1[byte >> 4] * sc);
+        o[i * 4 + j] = *reinterpret_cast<const uint32_t*>(&v);
+      }
+    uint4* dst = reinterpret_cast<uint4*>(kvt + (size_t)r * kRow + c * 32);
+#pragma unroll
+    for (int q = 0; q < 4; q++) dst[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+  }
+  for (int task = threadIdx.x; task < kBS * 8; task += blockDim.x) {
+    const int r = task >> 3, c = task & 7;               // 8 rope dims per task
+    const uint2 b = *reinterpret_cast<const uint2*>(st + r * kRow4 + 288 + c * 8);
+    const uint32_t w[2] = {b.x, b.y};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const __nv_bfloat162 v0 = __floats2bfloat162_rn(e4m3_to_f32(w[i] & 0xFF), e4m3_to_f32((w[i] >> 8) & 0xFF));
+      const __nv_bfloat162 v1 = __floats2bfloat162_rn(e4m3_to_f32((w[i] >> 16) & 0xFF), e4m3_to_f32(w[i] >> 24));
+      o[2 * i] = *reinterpret_cast<const uint32_t*>(&v0);
+      o[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&v1);
+    }
+    *reinterpret_cast<uint4*>(kvt + (size_t)r * kRow + kLat + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
 
 template <int MT>
 __global__ void __launch_bounds__(256, 1) mla_decode_kernel(MlaDecodeArgs p) {
   pdl_entry();
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  __nv_bfloat16* kvs = reinterpret_cast<__nv_bfloat16*>(smem_raw);                 // 2 blocks
-  __nv_bfloat16* qs = kvs + 2 * kBS * kRow;                                         // [16MT][584]
+  // bf16 cache: two 64-row tiles double-buffered by TMA.  NVFP4 cache: one bf16 tile
+  // plus two 22.5 KB staging buffers (TMA fills one while the other is expanded).
+  __nv_bfloat16* kvs = reinterpret_cast<__nv_bfloat16*>(smem_raw);
+  uint8_t* stage4 = smem_raw + (size_t)kBS * kRow * 2;
+  __nv_bfloat16* qs = p.nvfp4 ? reinterpret_cast<__nv_bfloat16*>(stage4 + 2 * kBlockBytes4)
+                              : kvs + 2 * kBS * kRow;                               // [16MT][584]
   __nv_bfloat16* ps = qs + 16 * MT * kRow;                                          // [16MT][72]
   float* red = reinterpret_cast<float*>(ps + 16 * MT * kPRow);                      // [8][16MT]
   uint64_t* bars = reinterpret_cast<uint64_t*>(red + 8 * 16 * MT);                  // [2]
@@ -79,7 +130,19 @@ __global__ void __launch_bounds__(256, 1) mla_decode_kernel(MlaDecodeArgs p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int R = 16 * MT;
   const int seq = p.seq_of_tok[tok];
-  const int L = p.pos_of_tok[tok] + 1;
+  // dense: the first pos+1 positions; sparse: the selected positions (a -1 terminated prefix of sel[tok])
+  int L = p.pos_of_tok[tok] + 1;
+  const int* selr = p.sel ? p.sel + (size_t)tok * p.sel_stride : nullptr;
+  if (selr) {
+    __shared__ int nsel;
+    if (threadIdx.x == 0) {
+      int n = 0;
+      while (n < p.sel_stride && selr[n] >= 0) n++;
+      nsel = n;
+    }
+    __syncthreads();
+    L = nsel;
+  }
   const int ntiles = (L + kBS - 1) / kBS;
   const int tps = max(2, (ntiles + p.nsplit - 1) / p.nsplit);   // >= 2 tiles: keeps the KV double buffer busy
   const int t_begin = split * tps, t_end = min(ntiles, t_begin + tps);
@@ -95,10 +158,31 @@ __global__ void __launch_bounds__(256, 1) mla_decode_kernel(MlaDecodeArgs p) {
   __syncthreads();
 
   auto issue = [&](int tile, int buf) {
+    if (selr) {     // gather the tile's selected rows one bulk copy each, all on one barrier
+      const int rb = p.nvfp4 ? kRow4 : kRow * 2;
+      mbar_expect_tx(&bars[buf], (uint32_t)(kBS * rb));
+      uint8_t* dst = p.nvfp4 ? stage4 + (size_t)buf * kBlockBytes4
+                             : reinterpret_cast<uint8_t*>(kvs + (size_t)buf * kBS * kRow);
+      const int first = selr[0];
+      for (int r = 0; r < kBS; r++) {
+        int pos = tile * kBS + r < L ? selr[tile * kBS + r] : first;   // masked rows re-read a valid row
+        int blk = p.block_table[(size_t)seq * p.bt_stride + pos / kBS];
+        if (blk < 0 || blk >= p.n_blocks || pos < 0) { set_status(p.status, kBadIndex); blk = 0; pos = 0; }
+        const size_t src_row = (size_t)blk * kBS + (pos % kBS);
+        bulk_g2s(dst + (size_t)r * rb, reinterpret_cast<const uint8_t*>(p.kv) + src_row * rb, rb, &bars[buf]);
+      }
+      return;
+    }
     int blk = p.block_table[(size_t)seq * p.bt_stride + tile];
     if (blk < 0 || blk >= p.n_blocks) { set_status(p.status, kBadIndex); blk = 0; }
-    mbar_expect_tx(&bars[buf], kBlockBytes);
-    bulk_g2s(kvs + (size_t)buf * kBS * kRow, p.kv + (size_t)blk * kBS * kRow, kBlockBytes, &bars[buf]);
+    if (p.nvfp4) {
+      mbar_expect_tx(&bars[buf], kBlockBytes4);
+      bulk_g2s(stage4 + (size_t)buf * kBlockBytes4,
+               reinterpret_cast<const uint8_t*>(p.kv) + (size_t)blk * kBlockBytes4, kBlockBytes4, &bars[buf]);
+    } else {
+      mbar_expect_tx(&bars[buf], kBlockBytes);
+      bulk_g2s(kvs + (size_t)buf * kBS * kRow, p.kv + (size_t)blk * kBS * kRow, kBlockBytes, &bars[buf]);
+    }
   };
   if (threadIdx.x == 0 && t_begin < t_end) issue(t_begin, 0);
 
@@ -120,6 +204,11 @@ __global__ void __launch_bounds__(256, 1) mla_decode_kernel(MlaDecodeArgs p) {
     phase[buf] ^= 1;
     if (!__syncthreads_and(ok)) { set_status(p.status, kTimeout); return; }
     const __nv_bfloat16* kvt = kvs + (size_t)buf * kBS * kRow;
+    if (p.nvfp4) {
+      expand_nvfp4_block(stage4 + (size_t)buf * kBlockBytes4, kvs);
+      __syncthreads();
+      kvt = kvs;
+    }
 
     // ---- S = Q K^T for positions [8w, 8w+8) of the tile ----
     float s[MT][4];
@@ -420,10 +509,12 @@ void mla_combine_uv(torch::Tensor o_part, torch::Tensor ml_part, torch::Tensor w
 
 void mla_decode(torch::Tensor q, torch::Tensor kv, torch::Tensor block_table, torch::Tensor seq_of_tok,
                 torch::Tensor pos_of_tok, torch::Tensor o_part, torch::Tensor ml_part, double scale,
-                torch::Tensor status) {
+                torch::Tensor status, c10::optional<torch::Tensor> sel) {
   const int T = q.size(0), Hh = q.size(1);
   TORCH_CHECK(q.size(2) == kQK && q.stride(2) == 1 && q.stride(1) == kQK, "mla_decode: q [T, Hh, 576]");
-  TORCH_CHECK(kv.size(1) == kBS && kv.size(2) == kRow && kv.is_contiguous(), "mla_decode: kv [blocks,64,584]");
+  const bool nv4 = kv.scalar_type() == at::kByte;
+  TORCH_CHECK(kv.size(1) == kBS && kv.size(2) == (nv4 ? kRow4 : kRow) && kv.is_contiguous(),
+              "mla_decode: kv [blocks,64,584] bf16 or [blocks,64,352] uint8 (NVFP4)");
   TORCH_CHECK(Hh <= 32, "mla_decode: at most 32 heads per rank");
   const int S = o_part.size(0);
   TORCH_CHECK(o_part.size(1) == T && o_part.size(2) == Hh && o_part.size(3) == kLat, "mla_decode: o_part shape");
@@ -436,17 +527,27 @@ void mla_decode(torch::Tensor q, torch::Tensor kv, torch::Tensor block_table, to
   p.o_part = o_part.data_ptr<float>(); p.ml_part = ml_part.data_ptr<float>();
   p.T = T; p.Hh = Hh; p.nsplit = S;
   p.scale_log2 = (float)(scale * 1.4426950408889634);
+  p.nvfp4 = nv4 ? 1 : 0;
+  p.sel = nullptr; p.sel_stride = 0;
+  if (sel.has_value() && sel->defined()) {
+    TORCH_CHECK(sel->scalar_type() == at::kInt && sel->dim() == 2 && sel->size(0) == T && sel->stride(1) == 1,
+                "mla_decode: sel [T, topk] int32");
+    p.sel = sel->data_ptr<int>(); p.sel_stride = sel->stride(0);
+    TORCH_CHECK(sel->size(1) == p.sel_stride, "mla_decode: sel rows must be contiguous");
+  }
   p.status = status.data_ptr<int>();
   auto stream = at::cuda::getCurrentCUDAStream();
   dim3 grid(T, S);
   if (Hh <= 16) {
     const int MT = 1;
-    size_t smem = (size_t)(2 * kBS * kRow + 16 * MT * kRow + 16 * MT * kPRow) * 2 + 8 * 16 * MT * 4 + 16;
+    size_t smem = (size_t)((nv4 ? 1 : 2) * kBS * kRow + 16 * MT * kRow + 16 * MT * kPRow) * 2 + 8 * 16 * MT * 4 + 16 +
+                  (nv4 ? 2 * kBlockBytes4 : 0);
     cudaFuncSetAttribute(mla_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     launch_k(mla_decode_kernel<1>, grid, 256, smem, stream, p);
   } else {
     const int MT = 2;
-    size_t smem = (size_t)(2 * kBS * kRow + 16 * MT * kRow + 16 * MT * kPRow) * 2 + 8 * 16 * MT * 4 + 16;
+    size_t smem = (size_t)((nv4 ? 1 : 2) * kBS * kRow + 16 * MT * kRow + 16 * MT * kPRow) * 2 + 8 * 16 * MT * 4 + 16 +
+                  (nv4 ? 2 * kBlockBytes4 : 0);
     cudaFuncSetAttribute(mla_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     launch_k(mla_decode_kernel<2>, grid, 256, smem, stream, p);
   }

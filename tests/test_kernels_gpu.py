@@ -466,3 +466,121 @@ def test_mla_combine_uv(C, T, Hh, S):
     ref = torch.einsum("thk,hjk->thj", olat, wd).reshape(T, Hh * 128)
     got = fp8.dequant_act_fp8(q.cpu().view(torch.float8_e4m3fn), qs.cpu())
     assert rel(got, ref) < 4e-2
+
+
+@pytest.mark.parametrize("Hh,ctx,nsplit", [(32, [1, 65, 300], 4), (8, [200], 2)])
+def test_mla_decode_nvfp4_cache(C, Hh, ctx, nsplit):
+    """Decode attention straight from 352-byte NVFP4 rows equals attention over
+    the rows' golden decode."""
+    g = torch.Generator().manual_seed(77 + Hh)
+    nseq = len(ctx)
+    maxb = max(-(-c // 64) for c in ctx)
+    nblk = nseq * maxb + 2
+    lat = torch.randn(nblk * 64, 512, generator=g)
+    rope = torch.randn(nblk * 64, 64, generator=g)
+    rows = kv_nvfp4.encode(lat, rope)                        # [nblk*64, 352]
+    kv4 = rows.view(nblk, 64, 352)
+    dl, dr = kv_nvfp4.decode(rows)
+    full = torch.cat([dl, dr], 1).view(nblk, 64, 576)
+    perm = torch.randperm(nblk - 1, generator=g)[: nseq * maxb] + 1
+    bt = perm.view(nseq, maxb).int()
+    q = (torch.randn(nseq, Hh, 576, generator=g) * 0.3).to(torch.bfloat16)
+    seq = torch.arange(nseq, dtype=torch.int32)
+    pos = torch.tensor([c - 1 for c in ctx], dtype=torch.int32)
+    opart = torch.empty(nsplit, nseq, Hh, 512, device=DEV)
+    ml = torch.empty(nsplit, nseq, Hh, 2, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    scale = 1 / math.sqrt(192)
+    C.mla_decode(q.to(DEV), kv4.contiguous().to(DEV), bt.to(DEV), seq.to(DEV), pos.to(DEV), opart, ml, scale, status)
+    out = torch.empty(nseq, Hh, 512, dtype=torch.bfloat16, device=DEV)
+    oq = torch.empty(nseq, Hh, 512, dtype=torch.uint8, device=DEV); os_ = torch.empty(nseq, Hh, 8, dtype=torch.uint8, device=DEV)
+    C.mla_combine(opart, ml, out, oq, os_)
+    assert int(status) == 0
+    for i, c in enumerate(ctx):
+        r = torch.cat([full[bt[i, p // 64], p % 64:p % 64 + 1] for p in range(c)]).to(torch.bfloat16).float()
+        s = (q[i].float() @ r.t()) * scale
+        ref = torch.softmax(s, -1) @ r[:, :512]
+        assert rel(out[i].cpu().float(), ref) < 2e-2, i
+
+
+# ------------------------------------------------------------------------- sparse attention (DSA indexer)
+@pytest.mark.parametrize("Hi,ctx", [(32, [130, 64, 1]), (8, [300])])
+def test_indexer_logits(C, Hi, ctx):
+    g = torch.Generator().manual_seed(Hi)
+    T = len(ctx)
+    maxb = max(-(-c // 64) for c in ctx)
+    nblk = T * maxb + 1
+    kc = (torch.randn(nblk, 64, 128, generator=g) * 0.3).to(torch.bfloat16)
+    bt = (torch.randperm(nblk - 1, generator=g)[: T * maxb] + 1).view(T, maxb).int()
+    q = (torch.randn(T, Hi, 128, generator=g) * 0.3).to(torch.bfloat16)
+    w = torch.randn(T, Hi, generator=g)
+    pos = torch.tensor([c - 1 for c in ctx], dtype=torch.int32)
+    S = maxb * 64
+    out = torch.empty(T, S, device=DEV)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    C.indexer_logits(q.to(DEV), w.to(DEV), kc.to(DEV), bt.to(DEV), torch.arange(T, dtype=torch.int32).to(DEV),
+                     pos.to(DEV), out, st)
+    assert int(st) == 0
+    for i, c in enumerate(ctx):
+        keys = torch.cat([kc[bt[i, p // 64], p % 64][None] for p in range(c)]).float()
+        ref = (torch.relu(q[i].float() @ keys.t()) * w[i][:, None]).sum(0)
+        got = out[i].cpu()
+        assert torch.allclose(got[:c], ref, rtol=2e-3, atol=2e-3)
+        assert bool(torch.isinf(got[c:]).all())
+
+
+@pytest.mark.parametrize("S,k", [(5000, 2048), (100, 2048), (4096, 7), (131072, 2048)])
+def test_indexer_topk(C, S, k):
+    g = torch.Generator().manual_seed(S + k)
+    x = torch.randn(3, S, generator=g)
+    x[1, S // 2:] = float("-inf")                 # a row with a causal tail
+    x[2, :: 3] = 0.5                               # many ties
+    out = torch.empty(3, k, dtype=torch.int32, device=DEV)
+    C.indexer_topk(x.to(DEV), k, out)
+    out = out.cpu()
+    for r in range(3):
+        fin = torch.isfinite(x[r])
+        n = min(k, int(fin.sum()))
+        sel = out[r][:n]
+        assert bool((out[r][n:] == -1).all())
+        assert bool((sel[1:] > sel[:-1]).all())  # increasing positions
+        # the selection is a valid top-n: its smallest value >= every unselected finite value
+        vals = x[r][sel.long()]
+        mask = torch.ones(S, dtype=torch.bool); mask[sel.long()] = False
+        rest = x[r][mask & fin]
+        if rest.numel():
+            assert float(vals.min()) >= float(rest.max())
+        # ties at the threshold are taken lowest-index first
+        thr = float(vals.min())
+        tied_unsel = ((x[r] == thr) & mask).nonzero().flatten()
+        tied_sel = sel[vals == thr]
+        if tied_unsel.numel() and tied_sel.numel():
+            assert int(tied_sel.max()) < int(tied_unsel.min())
+
+
+def test_sparse_mla_decode_selection(C):
+    """mla_decode over a selection list equals dense attention over the selected rows."""
+    g = torch.Generator().manual_seed(3)
+    Hh, nblk = 16, 9
+    kv = _paged_cache(nblk, g)
+    bt = torch.arange(1, nblk, dtype=torch.int32).view(1, 8)
+    ctx = 8 * 64
+    q = (torch.randn(2, Hh, 576, generator=g) * 0.3).to(torch.bfloat16)
+    sel = torch.full((2, 128), -1, dtype=torch.int32)
+    picks = [torch.randperm(ctx, generator=g)[:100].sort().values, torch.arange(0, 70)]
+    for i, pk in enumerate(picks):
+        sel[i, :len(pk)] = pk.int()
+    seq = torch.zeros(2, dtype=torch.int32)
+    pos = torch.full((2,), ctx - 1, dtype=torch.int32)
+    opart = torch.empty(4, 2, Hh, 512, device=DEV)
+    ml = torch.empty(4, 2, Hh, 2, device=DEV)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    scale = 1 / math.sqrt(192)
+    C.mla_decode(q.to(DEV), kv.to(DEV), bt.to(DEV), seq.to(DEV), pos.to(DEV), opart, ml, scale, st, sel.to(DEV))
+    out = torch.empty(2, Hh, 512, dtype=torch.bfloat16, device=DEV)
+    C.mla_combine(opart, ml, out, None, None)
+    assert int(st) == 0
+    for i, pk in enumerate(picks):
+        rows = torch.cat([kv[bt[0, p // 64], p % 64][None] for p in pk.tolist()])[:, :576].float()
+        ref = torch.softmax((q[i].float() @ rows.t()) * scale, -1) @ rows[:, :512]
+        assert rel(out[i].cpu().float(), ref) < 2e-2, i

@@ -77,3 +77,17 @@ def test_decode_tracks_reference_greedy(llm):
         top = float(row.max())
         assert float(row[tok]) >= top - 0.05 * (float(row.std()) + 1e-6) * 10, (tok, int(row.argmax()))
         toks.append(tok)
+
+
+def test_nvfp4_kv_engine_tracks_bf16_engine(llm):
+    """The same model with a 352 B/token NVFP4 latent cache: prefill logits equal
+    (the cache is not read in prefill) and the decode stays deterministic."""
+    nv = LLM(small_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=1024, max_num_seqs=4,
+             kv_cache_dtype="nvfp4")
+    p = [_prompt(40, 11)]
+    sp = SamplingParams(max_tokens=10, ignore_eos=True)
+    a = nv.generate(p, sp)[0].outputs[0].token_ids
+    b = nv.generate(p, sp)[0].outputs[0].token_ids
+    ref = llm.generate(p, sp)[0].outputs[0].token_ids
+    assert a == b and len(a) == 10
+    assert a[0] == ref[0]

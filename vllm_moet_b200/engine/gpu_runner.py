@@ -89,11 +89,13 @@ class NativeRunner:
         cfg = self.cfg
         self.num_blocks = num_blocks
         self.kv_mode = 2 if ecfg.kv_cache_dtype == "nvfp4" else 1
-        if self.kv_mode == 2:
-            raise NotImplementedError("NVFP4 KV decode attention is not wired in the native runner yet")
         n_cache = len(mw.layers) + (1 if mw.mtp is not None else 0)
-        self.kv = [torch.zeros(num_blocks, KV_BLOCK, BF16_ROW, dtype=torch.bfloat16, device=self.dev)
-                   for _ in range(n_cache)]
+        if self.kv_mode == 2:      # NVFP4 latent cache: 352 bytes per token (3.3x the context of bf16 rows)
+            self.kv = [torch.zeros(num_blocks, KV_BLOCK, NVFP4_ROW, dtype=torch.uint8, device=self.dev)
+                       for _ in range(n_cache)]
+        else:
+            self.kv = [torch.zeros(num_blocks, KV_BLOCK, BF16_ROW, dtype=torch.bfloat16, device=self.dev)
+                       for _ in range(n_cache)]
         self.cos_sin = rope_cos_sin(cfg, ecfg.max_model_len + 64, self.dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.miss = torch.zeros(1, dtype=torch.int32, device=self.dev)
