@@ -51,6 +51,7 @@ void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::
 void indexer_logits(torch::Tensor q, torch::Tensor w, torch::Tensor k_cache, torch::Tensor block_table,
                     torch::Tensor seq_of_tok, torch::Tensor pos_of_tok, torch::Tensor out, torch::Tensor status);
 void indexer_topk(torch::Tensor scores, int64_t k, torch::Tensor out);
+void idx_k_write(torch::Tensor k, torch::Tensor slot, torch::Tensor cache, torch::Tensor status);
 // bf12.cu
 void bf12_decode(torch::Tensor cls, torch::Tensor lo, torch::Tensor lut, torch::Tensor esc_pos, torch::Tensor esc_hi,
                  torch::Tensor out);
@@ -145,6 +146,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bf12_decode", &bf12_decode);
   m.def("indexer_logits", &indexer_logits);
   m.def("indexer_topk", &indexer_topk);
+  m.def("idx_k_write", &idx_k_write);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);

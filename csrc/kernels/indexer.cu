@@ -194,9 +194,32 @@ __global__ void __launch_bounds__(kTopkThreads) indexer_topk_kernel(const float*
   for (int i = total + threadIdx.x; i < k; i += blockDim.x) orow[i] = -1;
 }
 
+// Indexer key cache insert: cache[slot[t]] = k[t] (bf16 rows of D); slot < 0 skips.
+__global__ void idx_k_write_kernel(const __nv_bfloat16* __restrict__ k, int D, const long long* __restrict__ slot,
+                                   long long n_slots, __nv_bfloat16* __restrict__ cache, int* __restrict__ status) {
+  pdl_entry();
+  const long long s = slot[blockIdx.x];
+  if (s < 0) return;
+  if (s >= n_slots) { if (threadIdx.x == 0) set_status(status, kBadIndex); return; }
+  for (int i = threadIdx.x * 8; i < D; i += blockDim.x * 8)
+    *reinterpret_cast<uint4*>(cache + s * D + i) = *reinterpret_cast<const uint4*>(k + (size_t)blockIdx.x * D + i);
+}
+
 }  // namespace moet
 
 using namespace moet;
+
+void idx_k_write(torch::Tensor k, torch::Tensor slot, torch::Tensor cache, torch::Tensor status) {
+  const int T = k.size(0), D = k.size(1);
+  TORCH_CHECK(k.scalar_type() == at::kBFloat16 && k.is_contiguous() && D % 8 == 0 && cache.size(-1) == D &&
+              slot.scalar_type() == at::kLong, "idx_k_write: k [T, D] bf16, slot int64");
+  if (T == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  launch_k(idx_k_write_kernel, T, 32, 0, stream, (const __nv_bfloat16*)k.data_ptr(), D,
+           (const long long*)slot.data_ptr<int64_t>(), (long long)(cache.numel() / D),
+           (__nv_bfloat16*)cache.data_ptr(), status.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 
 void indexer_logits(torch::Tensor q, torch::Tensor w, torch::Tensor k_cache, torch::Tensor block_table,
                     torch::Tensor seq_of_tok, torch::Tensor pos_of_tok, torch::Tensor out, torch::Tensor status) {

@@ -91,3 +91,20 @@ def test_nvfp4_kv_engine_tracks_bf16_engine(llm):
     ref = llm.generate(p, sp)[0].outputs[0].token_ids
     assert a == b and len(a) == 10
     assert a[0] == ref[0]
+
+
+def test_indexer_engine(llm):
+    """DSA indexer + sparse MLA decode: with top-k >= the context the selection is
+    every position, so tokens equal the dense engine's; a small top-k still runs
+    deterministically."""
+    p = [_prompt(45, 21)]
+    sp = SamplingParams(max_tokens=8, ignore_eos=True)
+    ref = llm.generate(p, sp)[0].outputs[0].token_ids
+    full = LLM(small_cfg().replace(index_heads=8, index_topk=2048), device="cuda", num_speculative_tokens=2,
+               max_model_len=1024, max_num_seqs=4)
+    assert full.generate(p, sp)[0].outputs[0].token_ids == ref
+    del full
+    sparse = LLM(small_cfg().replace(index_heads=8, index_topk=16), device="cuda", num_speculative_tokens=2,
+                 max_model_len=1024, max_num_seqs=4)
+    a = sparse.generate(p, sp)[0].outputs[0].token_ids
+    assert a == sparse.generate(p, sp)[0].outputs[0].token_ids and len(a) == 8

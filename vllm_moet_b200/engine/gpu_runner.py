@@ -97,6 +97,10 @@ class NativeRunner:
             self.kv = [torch.zeros(num_blocks, KV_BLOCK, BF16_ROW, dtype=torch.bfloat16, device=self.dev)
                        for _ in range(n_cache)]
         self.cos_sin = rope_cos_sin(cfg, ecfg.max_model_len + 64, self.dev)
+        # DSA indexer key caches (bf16 [blocks, 64, D] per layer with an indexer)
+        self.idx_kv = [torch.zeros(num_blocks, KV_BLOCK, cfg.index_head_dim, dtype=torch.bfloat16, device=self.dev)
+                       if lw.idx_wq is not None else None
+                       for lw in list(mw.layers) + ([mw.mtp.layer] if mw.mtp is not None else [])]
         self.status = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.miss = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.ws_decode_by_bucket = {}
@@ -303,6 +307,7 @@ class NativeRunner:
         C.rmsnorm_quant(qkva[:, :ql], None, None, lw.q_a_norm, cfg.rms_eps, None, qaq, qas, None, None, 0)
         qb = self.ws.get("qb", (T, Hh * (nope + rope)), torch.bfloat16)
         self._gemv(qaq, qas, lw.q_b, qb)
+        sel = self._indexer(lw, hq, hs, qaq, qas, ctx, li) if lw.idx_wq is not None else None
         if ctx.mode == "decode":
             qnq = self.ws.get("qn.q", (T, Hh, nope), torch.uint8)
             qns = self.ws.get("qn.s", (T, Hh, nope // 64), torch.uint8)
@@ -314,7 +319,7 @@ class NativeRunner:
             S = max(1, min(32, 256 // T))
             opart = self.ws.get("opart", (S, T, Hh, lat), torch.float32)
             mlp = self.ws.get("mlpart", (S, T, Hh, 2), torch.float32)
-            C.mla_decode(qcat, cache, ctx.block_table, ctx.seq, ctx.pos, opart, mlp, self.scale, self.status)
+            C.mla_decode(qcat, cache, ctx.block_table, ctx.seq, ctx.pos, opart, mlp, self.scale, self.status, sel)
             # split merge + W_uv + e4m3 quantisation in one kernel
             C.mla_combine_uv(opart, mlp, lw.w_uv.w, lw.w_uv.s, ovq, ovs)
         else:
@@ -329,6 +334,30 @@ class NativeRunner:
             C.mla_prefill(qf, kvb.view(T, Hh, nope + vd), kr, ctx.cu_seqlens, ctx.max_len, self.scale,
                           ovq, ovs, None)
         self._row_parallel_out(ovq, ovs, lw.o, x, out, T)
+
+    def _indexer(self, lw, hq, hs, qaq, qas, ctx, li):
+        """DSA indexer: insert this step's keys, score every cached position
+        (head-weighted ReLU dot products), keep the top-k.  Decode returns the
+        selection for the sparse MLA decode; prefill only fills the key cache
+        (prefill attention is dense and causal)."""
+        cfg, C, T = self.cfg, self.C, ctx.T
+        Hi, Di = cfg.index_heads, cfg.index_head_dim
+        ki = self.ws.get("idx.k", (T, Di), torch.bfloat16)
+        self._gemv(hq, hs, lw.idx_wk, ki)
+        C.idx_k_write(ki, ctx.slot, self.idx_kv[li], self.status)
+        if ctx.mode != "decode":
+            return None
+        qi = self.ws.get("idx.q", (T, Hi * Di), torch.bfloat16)
+        self._gemv(qaq, qas, lw.idx_wq, qi)
+        wi = self.ws.get("idx.w", (T, Hi), torch.float32)
+        self._gemv(hq, hs, lw.idx_ww, wi)
+        S = ctx.block_table.shape[1] * KV_BLOCK
+        scores = self.ws.get("idx.scores", (T, S), torch.float32)
+        C.indexer_logits(qi.view(T, Hi, Di), wi, self.idx_kv[li], ctx.block_table, ctx.seq, ctx.pos, scores,
+                         self.status)
+        sel = self.ws.get("idx.sel", (T, cfg.index_topk), torch.int32)
+        C.indexer_topk(scores, cfg.index_topk, sel)
+        return sel
 
     def _ffn(self, lw: LayerWeights, x, ctx: StepCtx, out):
         cfg, C, T = self.cfg, self.C, ctx.T
@@ -526,7 +555,7 @@ class NativeRunner:
         xm = self.ws.get("xm", (T, H), torch.bfloat16)
         self._gemv(ehq, ehs, m.eh_proj, xm)
         self._check("mtp eh_proj", xm)
-        x = self._layer(m.layer, xm, ctx, self.kv[-1], 0)
+        x = self._layer(m.layer, xm, ctx, self.kv[-1], len(self.mw.layers))
         if rows is not None:      # only these rows need the head (e.g. the last row of each prompt)
             x = x[rows].contiguous()
         return self._final(x, None, "mtp")

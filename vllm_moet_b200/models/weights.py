@@ -163,8 +163,9 @@ class LayerWeights:
     w_uk_t: Optional[Fp8Linear] = None          # [Hh, kv_lora, nope]
     w_uv: Optional[Fp8Linear] = None            # [Hh, v, kv_lora]
     # sparse indexer (GLM shape)
-    idx_wq: object = None
-    idx_wk: object = None
+    idx_wq: object = None          # [Hi*D, q_lora] indexer queries (from the normed q_a)
+    idx_wk: object = None          # [D, H] indexer key (from the normed hidden)
+    idx_ww: object = None          # [Hi, H] per-head weights (softmax-free, scaled by 1/sqrt(Hi*D))
 
     @property
     def is_moe(self) -> bool:
@@ -325,6 +326,13 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
     )
     if isinstance(lw.kv_b, Fp8Linear):
         lw.w_uk_t, lw.w_uv = _derive_absorb(lw.kv_b, cfg, Hh)
+    if cfg.index_heads:     # DSA indexer (replicated across TP ranks); its own draw stream
+        Hi, Di = cfg.index_heads, cfg.index_head_dim
+        saved, rng.counter = rng.counter, 1000 * (li + 1) + 900
+        lw.idx_wq = lin(rng.normal((Hi * Di, q_lora)))
+        lw.idx_wk = lin(rng.normal((Di, H)))
+        lw.idx_ww = lin(rng.normal((Hi, H)) / math.sqrt(Hi * Di))
+        rng.counter = saved
     if not moe:
         I = cfg.dense_intermediate
         Ip = tp_ffn_shard(I, tp_size, dt) if tp_size > 1 else I
