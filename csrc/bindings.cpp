@@ -47,6 +47,9 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
 void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::optional<torch::Tensor> resid,
                  c10::optional<torch::Tensor> shared_out, c10::optional<torch::Tensor> out,
                  c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> ar);
+// gemv_stream.cu
+void gemv_stream_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tensor sw, torch::Tensor out,
+                     c10::optional<torch::Tensor> resid, torch::Tensor status);
 // indexer.cu
 void indexer_logits(torch::Tensor q, torch::Tensor w, torch::Tensor k_cache, torch::Tensor block_table,
                     torch::Tensor seq_of_tok, torch::Tensor pos_of_tok, torch::Tensor out, torch::Tensor status);
@@ -146,6 +149,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bf12_decode", &bf12_decode);
   m.def("indexer_logits", &indexer_logits);
   m.def("indexer_topk", &indexer_topk);
+  m.def("gemv_stream_fp8", &gemv_stream_fp8);
   m.def("idx_k_write", &idx_k_write);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);

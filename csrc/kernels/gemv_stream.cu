@@ -1,0 +1,193 @@
+// Persistent, TMA-fed FP8 GEMV for decode: out[T, N] = A[T, K] * W[N, K]^T,
+// W e4m3 row-major with UE8M0 128x128 block scales, A e4m3 with UE8M0 per-64
+// scales, T <= 8 tokens.
+//
+// The weight-streaming GEMV in gemv_fp8.cu issues one batch of loads per CTA
+// and retires; at 3 tokens it reaches ~2 TB/s, latency-bound by CTA waves.
+// Here each SM runs one persistent CTA that streams 16-row weight blocks
+// through a ring of shared-memory stages filled by cp.async.bulk (one copy
+// per row, rows padded by 16 bytes so ldmatrix is conflict-free) completing
+// on mbarriers, kRing stages in flight, so HBM sees a continuous stream.
+// Eight warps split each block's K range; each takes m16n8k32 e4m3 MMAs with
+// the weight rows as A (ldmatrix.x4) and the tokens as B (ldmatrix.x2 from
+// the activation rows staged once in shared memory), applies the weight and
+// activation scales per 64-k chunk, and the warps' partial sums are reduced
+// through shared memory before the next block.  All waits are bounded.
+#include "common.cuh"
+#include "torch_glue.h"
+
+namespace moet {
+
+namespace gs {
+constexpr int kRows = 16;        // rows per stage
+constexpr int kWarps = 8;
+constexpr int kMaxRing = 4;      // stages in flight (as many as fit in shared memory, >= 2)
+constexpr int kMaxK = 8192;
+constexpr int kMaxT = 8;
+
+MOET_DEVICE uint32_t s32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+MOET_DEVICE void bar_init(uint64_t* b, int n) { asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(s32(b)), "r"(n)); }
+MOET_DEVICE void bar_expect(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s32(b)), "r"(bytes));
+}
+MOET_DEVICE bool bar_try(uint64_t* b, uint32_t par) {
+  uint32_t ok;
+  asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+               : "=r"(ok) : "r"(s32(b)), "r"(par) : "memory");
+  return ok != 0;
+}
+MOET_DEVICE bool bar_wait(uint64_t* b, uint32_t par) {
+  for (uint32_t i = 0; i < (1u << 22); i++)
+    if (bar_try(b, par)) return true;
+  return false;
+}
+MOET_DEVICE void bulk(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(s32(dst)), "l"(src), "r"(bytes), "r"(s32(b)) : "memory");
+}
+}  // namespace gs
+
+struct GemvStreamArgs {
+  const uint8_t* A; const uint8_t* sA; long long a_stride, sa_stride;
+  const uint8_t* W; const uint8_t* sW; int sw_cols;
+  void* out; long long out_stride; int out_f32;
+  const __nv_bfloat16* resid;
+  int T, N, K;
+  int ring;
+  int* status;
+};
+
+__global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStreamArgs p) {
+  using namespace gs;
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int KP = p.K + 16;                                  // padded row stride (bytes)
+  const int kRing = p.ring;
+  uint8_t* ring = sm;                                       // kRing x [16][KP]
+  uint8_t* xs = ring + (size_t)kRing * kRows * KP;          // [8][KP] activations
+  float* red = reinterpret_cast<float*>(xs + (size_t)kMaxT * KP);   // [warps][16][8]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red + 2 * kWarps * kRows * kMaxT);   // red: 2 buffers
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int nblocks = (p.N + kRows - 1) / kRows;
+  const int first = blockIdx.x, step = gridDim.x;
+  const int nmine = first < nblocks ? (nblocks - first + step - 1) / step : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRing; s++) bar_init(&bars[s], 1);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+  auto issue = [&](int i) {      // i-th block of this CTA -> stage i % kRing
+    const int rb = first + i * step, s = i % kRing;
+    const int r0 = rb * kRows, nr = min(kRows, p.N - r0);
+    bar_expect(&bars[s], (uint32_t)(nr * p.K));
+    for (int r = 0; r < nr; r++)
+      bulk(ring + ((size_t)s * kRows + r) * KP, p.W + (size_t)(r0 + r) * p.K, (uint32_t)p.K, &bars[s]);
+  };
+  // weights are immutable: start the stream before waiting on the previous kernel
+  if (threadIdx.x == 0)
+    for (int i = 0; i < min(kRing, nmine); i++) issue(i);
+  pdl_entry();
+  // activations (zero rows beyond T) -> shared memory
+  for (int i = threadIdx.x; i < kMaxT * (p.K / 16); i += blockDim.x) {
+    const int r = i / (p.K / 16), c = (i % (p.K / 16)) * 16;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < p.T) v = *reinterpret_cast<const uint4*>(p.A + (size_t)r * p.a_stride + c);
+    *reinterpret_cast<uint4*>(xs + (size_t)r * KP + c) = v;
+  }
+  __syncthreads();
+  const int nchunks = p.K / 64;
+  const int cpw = (nchunks + kWarps - 1) / kWarps;          // 64-k chunks per warp
+  const int c_lo = warp * cpw, c_hi = min(nchunks, c_lo + cpw);
+  for (int i = 0; i < nmine; i++) {
+    const int s = i % kRing;
+    const int rb = first + i * step, r0 = rb * kRows;
+    const uint8_t* swr = p.sW + (size_t)(r0 >> 7) * p.sw_cols;
+    const bool ok = bar_wait(&bars[s], (uint32_t)((i / kRing) & 1));
+    if (!__syncthreads_and(ok)) {
+      if (threadIdx.x == 0) set_status(p.status, kTimeout);
+      return;
+    }
+    const uint8_t* wst = ring + (size_t)s * kRows * KP;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = c_lo; c < c_hi; c++) {
+      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t a[4], b[2];
+      ldmatrix_x4(a, wst + (size_t)(lane & 15) * KP + c * 64 + (lane >> 4) * 16);
+      ldmatrix_x2(b, xs + (size_t)(lane & 7) * KP + c * 64 + ((lane >> 3) & 1) * 16);
+      mma_e4m3_16832(d0, a, b[0], b[1], d0);
+      ldmatrix_x4(a, wst + (size_t)(lane & 15) * KP + c * 64 + 32 + (lane >> 4) * 16);
+      ldmatrix_x2(b, xs + (size_t)(lane & 7) * KP + c * 64 + 32 + ((lane >> 3) & 1) * 16);
+      mma_e4m3_16832(d1, a, b[0], b[1], d1);
+      const float ws = ue8m0_to_float(swr[c >> 1]);
+      const float s0 = 2 * t < p.T ? ws * ue8m0_to_float(p.sA[(size_t)(2 * t) * p.sa_stride + c]) : 0.f;
+      const float s1 = 2 * t + 1 < p.T ? ws * ue8m0_to_float(p.sA[(size_t)(2 * t + 1) * p.sa_stride + c]) : 0.f;
+      acc[0] = fmaf(d0[0] + d1[0], s0, acc[0]);
+      acc[1] = fmaf(d0[1] + d1[1], s1, acc[1]);
+      acc[2] = fmaf(d0[2] + d1[2], s0, acc[2]);
+      acc[3] = fmaf(d0[3] + d1[3], s1, acc[3]);
+    }
+    // partial sums -> red[i & 1]; one barrier frees stage s and publishes red
+    float* rw = red + ((size_t)(i & 1) * kWarps + warp) * kRows * kMaxT;
+    rw[g * kMaxT + 2 * t] = acc[0];
+    rw[g * kMaxT + 2 * t + 1] = acc[1];
+    rw[(g + 8) * kMaxT + 2 * t] = acc[2];
+    rw[(g + 8) * kMaxT + 2 * t + 1] = acc[3];
+    __syncthreads();
+    if (threadIdx.x == 0 && i + kRing < nmine) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(i + kRing);
+    }
+    const float* rr = red + (size_t)(i & 1) * kWarps * kRows * kMaxT;
+    for (int o = threadIdx.x; o < kRows * kMaxT; o += blockDim.x) {
+      const int row = o / kMaxT, tok = o % kMaxT;
+      if (tok >= p.T || r0 + row >= p.N) continue;
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; w++) v += rr[(size_t)w * kRows * kMaxT + o];
+      const size_t off = (size_t)tok * p.out_stride + r0 + row;
+      if (p.resid) v += __bfloat162float(p.resid[off]);
+      if (p.out_f32) reinterpret_cast<float*>(p.out)[off] = v;
+      else reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16(v);
+    }
+  }
+}
+
+}  // namespace moet
+
+using namespace moet;
+
+// Same contract as gemv_fp8 for unbatched weights, T <= 8, K % 64 == 0, K <= 8192.
+void gemv_stream_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tensor sw, torch::Tensor out,
+                     c10::optional<torch::Tensor> resid, torch::Tensor status) {
+  const int T = a.size(0), K = w.size(1), N = w.size(0);
+  TORCH_CHECK(w.dim() == 2 && w.is_contiguous() && K % 128 == 0 && K <= gs::kMaxK && T <= gs::kMaxT,
+              "gemv_stream_fp8: W [N, K] contiguous, K % 128 == 0, K <= 8192, T <= 8");
+  TORCH_CHECK(a.size(1) == K && a.stride(1) == 1 && a.stride(0) % 16 == 0 && sa.stride(1) == 1, "gemv_stream_fp8: A");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0,
+              "gemv_stream_fp8: 16-byte aligned operands");
+  TORCH_CHECK(out.stride(1) == 1 && (out.scalar_type() == at::kFloat || out.scalar_type() == at::kBFloat16),
+              "gemv_stream_fp8: out bf16 or f32");
+  if (T == 0) return;
+  GemvStreamArgs p;
+  p.A = (const uint8_t*)a.data_ptr(); p.sA = (const uint8_t*)sa.data_ptr(); p.a_stride = a.stride(0);
+  p.sa_stride = sa.stride(0);
+  p.W = (const uint8_t*)w.data_ptr(); p.sW = (const uint8_t*)sw.data_ptr(); p.sw_cols = sw.size(1);
+  p.out = out.data_ptr(); p.out_stride = out.stride(0); p.out_f32 = out.scalar_type() == at::kFloat;
+  p.resid = resid.has_value() && resid->defined() ? (const __nv_bfloat16*)resid->data_ptr() : nullptr;
+  if (p.resid) TORCH_CHECK(resid->stride(0) == out.stride(0), "gemv_stream_fp8: resid layout");
+  p.T = T; p.N = N; p.K = K; p.status = status.data_ptr<int>();
+  const int KP = K + 16;
+  const size_t fixed = (size_t)gs::kMaxT * KP + (size_t)2 * gs::kWarps * gs::kRows * gs::kMaxT * 4 + gs::kMaxRing * 8;
+  const size_t budget = 220 * 1024;
+  const int ring = (int)std::min<size_t>(gs::kMaxRing, (budget - fixed) / ((size_t)gs::kRows * KP));
+  TORCH_CHECK(ring >= 2, "gemv_stream_fp8: K too large for a 2-stage ring");
+  p.ring = ring;
+  const size_t smem = (size_t)ring * gs::kRows * KP + fixed;
+  static int n_sm = 0;
+  if (!n_sm) cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, 0);
+  const int nblocks = (N + gs::kRows - 1) / gs::kRows;
+  cudaFuncSetAttribute(gemv_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  launch_k(gemv_stream_kernel, std::min(nblocks, n_sm), gs::kWarps * 32, smem, stream, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

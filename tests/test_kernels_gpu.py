@@ -584,3 +584,25 @@ def test_sparse_mla_decode_selection(C):
         rows = torch.cat([kv[bt[0, p // 64], p % 64][None] for p in pk.tolist()])[:, :576].float()
         ref = torch.softmax((q[i].float() @ rows.t()) * scale, -1) @ rows[:, :512]
         assert rel(out[i].cpu().float(), ref) < 2e-2, i
+
+
+@pytest.mark.parametrize("T,N,K", [(1, 1600, 4096), (3, 4096, 4096), (8, 1000, 1024), (3, 130, 1536), (5, 16160, 2048)])
+def test_gemv_stream_matches_gemv(C, T, N, K):
+    g = torch.Generator().manual_seed(N + K + T)
+    from vllm_moet_b200.models.weights import Fp8Linear
+    lin = Fp8Linear.from_float(torch.randn(N, K, generator=g) * 0.05)
+    x = torch.randn(T, K, generator=g)
+    aq, sa = fp8.quant_act_fp8(x)
+    aq = aq.view(torch.uint8).to(DEV); sa = sa.to(DEV)
+    w, sw = lin.w.to(DEV), lin.s.to(DEV)
+    ref = torch.empty(T, N, device=DEV)
+    C.gemv_fp8(aq, sa, w, sw, ref, None)
+    out = torch.empty(T, N, device=DEV)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    C.gemv_stream_fp8(aq, sa, w, sw, out, None, st)
+    assert int(st) == 0
+    assert torch.allclose(out, ref, rtol=1e-4, atol=1e-3), float((out - ref).abs().max())
+    resid = torch.randn(T, N, generator=g).to(torch.bfloat16).to(DEV)
+    ob = torch.empty(T, N, dtype=torch.bfloat16, device=DEV)
+    C.gemv_stream_fp8(aq, sa, w, sw, ob, resid, st)
+    assert torch.allclose(ob.float(), (ref + resid.float()), rtol=2e-2, atol=2e-2)

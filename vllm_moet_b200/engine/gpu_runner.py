@@ -124,6 +124,7 @@ class NativeRunner:
         import os
         self.debug_finite = os.environ.get("MOET_DEBUG_FINITE", "0") == "1"
         self.branches = os.environ.get("MOET_BRANCHES", "1") != "0"
+        self.gemv_stream = os.environ.get("MOET_GEMV_STREAM", "1") != "0"
 
     # ------------------------------------------------------------------ helpers
     @staticmethod
@@ -161,6 +162,10 @@ class NativeRunner:
                 return
         if T > 128 and K % 128 == 0 and lin.w.dim() == 2 and aq.stride(0) % 16 == 0:
             self.C.tc_gemm_fp8(aq, as_, lin.w, lin.s, out, resid, 128, self.status)
+        elif (T <= 8 and lin.w.dim() == 2 and K % 128 == 0 and K <= 6144 and aq.stride(0) % 16 == 0
+              and self.gemv_stream):
+            # persistent TMA-ring GEMV: weight rows stream through shared memory continuously
+            self.C.gemv_stream_fp8(aq, as_, lin.w, lin.s, out, resid, self.status)
         else:
             self.C.gemv_fp8(aq, as_, lin.w, lin.s, out, resid)
 
