@@ -48,8 +48,9 @@ void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::
                  c10::optional<torch::Tensor> shared_out, c10::optional<torch::Tensor> out,
                  c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> ar);
 // gemv_stream.cu
-void gemv_stream_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tensor sw, torch::Tensor out,
-                     c10::optional<torch::Tensor> resid, torch::Tensor status);
+void gemv_stream_fp8(c10::optional<torch::Tensor> a, c10::optional<torch::Tensor> sa, torch::Tensor w,
+                     torch::Tensor sw, torch::Tensor out, c10::optional<torch::Tensor> resid, torch::Tensor status,
+                     c10::optional<torch::Tensor> x_norm, c10::optional<torch::Tensor> gamma, double eps);
 // indexer.cu
 void indexer_logits(torch::Tensor q, torch::Tensor w, torch::Tensor k_cache, torch::Tensor block_table,
                     torch::Tensor seq_of_tok, torch::Tensor pos_of_tok, torch::Tensor out, torch::Tensor status);
@@ -149,7 +150,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bf12_decode", &bf12_decode);
   m.def("indexer_logits", &indexer_logits);
   m.def("indexer_topk", &indexer_topk);
-  m.def("gemv_stream_fp8", &gemv_stream_fp8);
+  m.def("gemv_stream_fp8", &gemv_stream_fp8, py::arg("a"), py::arg("sa"), py::arg("w"), py::arg("sw"), py::arg("out"),
+        py::arg("resid"), py::arg("status"), py::arg("x_norm") = py::none(), py::arg("gamma") = py::none(),
+        py::arg("eps") = 1e-6);
   m.def("idx_k_write", &idx_k_write);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);

@@ -55,6 +55,8 @@ struct GemvStreamArgs {
   int T, N, K;
   int ring;
   int* status;
+  // optional fused RMSNorm + e4m3 quantisation of a bf16 input (replaces A / sA)
+  const __nv_bfloat16* xin; long long xin_stride; const __nv_bfloat16* gamma; float eps;
 };
 
 __global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStreamArgs p) {
@@ -65,7 +67,8 @@ __global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStr
   uint8_t* ring = sm;                                       // kRing x [16][KP]
   uint8_t* xs = ring + (size_t)kRing * kRows * KP;          // [8][KP] activations
   float* red = reinterpret_cast<float*>(xs + (size_t)kMaxT * KP);   // [warps][16][8]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(red + 2 * kWarps * kRows * kMaxT);   // red: 2 buffers
+  float* sas = red + 2 * kWarps * kRows * kMaxT;            // [8][K/64] activation scales (as floats)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sas + kMaxT * (kMaxK / 64));   // red: 2 buffers
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int nblocks = (p.N + kRows - 1) / kRows;
   const int first = blockIdx.x, step = gridDim.x;
@@ -87,12 +90,77 @@ __global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStr
   if (threadIdx.x == 0)
     for (int i = 0; i < min(kRing, nmine); i++) issue(i);
   pdl_entry();
-  // activations (zero rows beyond T) -> shared memory
-  for (int i = threadIdx.x; i < kMaxT * (p.K / 16); i += blockDim.x) {
-    const int r = i / (p.K / 16), c = (i % (p.K / 16)) * 16;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < p.T) v = *reinterpret_cast<const uint4*>(p.A + (size_t)r * p.a_stride + c);
-    *reinterpret_cast<uint4*>(xs + (size_t)r * KP + c) = v;
+  const int ng = p.K / 64;
+  if (p.xin == nullptr) {
+    // activations (zero rows beyond T) -> shared memory
+    for (int i = threadIdx.x; i < kMaxT * (p.K / 16); i += blockDim.x) {
+      const int r = i / (p.K / 16), c = (i % (p.K / 16)) * 16;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (r < p.T) v = *reinterpret_cast<const uint4*>(p.A + (size_t)r * p.a_stride + c);
+      *reinterpret_cast<uint4*>(xs + (size_t)r * KP + c) = v;
+    }
+    for (int i = threadIdx.x; i < kMaxT * ng; i += blockDim.x) {
+      const int r = i / ng, c = i % ng;
+      sas[i] = r < p.T ? ue8m0_to_float(p.sA[(size_t)r * p.sa_stride + c]) : 0.f;
+    }
+  } else {
+    // fused RMSNorm + quantisation: one thread per (row, 64-group); the rounding
+    // follows rmsnorm_quant (bf16 module output, then e4m3 with a UE8M0 scale)
+    float* ssq = red;                                       // [T][ng] partial sums of squares
+    for (int i = threadIdx.x; i < p.T * ng; i += blockDim.x) {
+      const int r = i / ng, c = i % ng;
+      const uint4* xr = reinterpret_cast<const uint4*>(p.xin + (size_t)r * p.xin_stride + c * 64);
+      float acc = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const uint4 v = xr[u];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int q = 0; q < 4; q++) { const float2 f = __bfloat1622float2(h[q]); acc = fmaf(f.x, f.x, fmaf(f.y, f.y, acc)); }
+      }
+      ssq[i] = acc;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kMaxT * ng; i += blockDim.x) {
+      const int r = i / ng, c = i % ng;
+      uint8_t* dst = xs + (size_t)r * KP + c * 64;
+      if (r >= p.T) {
+        for (int b = 0; b < 64; b += 16) *reinterpret_cast<uint4*>(dst + b) = make_uint4(0, 0, 0, 0);
+        sas[i] = 0.f;
+        continue;
+      }
+      float tot = 0.f;
+      for (int q = 0; q < ng; q++) tot += ssq[r * ng + q];
+      const float rinv = rsqrtf(tot / (float)p.K + p.eps);
+      const uint4* xr = reinterpret_cast<const uint4*>(p.xin + (size_t)r * p.xin_stride + c * 64);
+      const uint4* gr = reinterpret_cast<const uint4*>(p.gamma + c * 64);
+      float y[64];
+      float amax = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const uint4 v = xr[u], gv = gr[u];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+        const __nv_bfloat162* gg = reinterpret_cast<const __nv_bfloat162*>(&gv);
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const float2 f = __bfloat1622float2(h[q]), g2 = __bfloat1622float2(gg[q]);
+          const float a = __bfloat162float(__float2bfloat16(f.x * rinv * g2.x));
+          const float b = __bfloat162float(__float2bfloat16(f.y * rinv * g2.y));
+          y[u * 8 + 2 * q] = a; y[u * 8 + 2 * q + 1] = b;
+          amax = fmaxf(amax, fmaxf(fabsf(a), fabsf(b)));
+        }
+      }
+      const uint32_t e = ue8m0_for_amax(amax);
+      const float inv = (e >= 1 && e <= 253) ? __uint_as_float((254u - e) << 23) : 0.f;
+#pragma unroll
+      for (int b = 0; b < 64; b += 16) {
+        uint8_t o[16];
+#pragma unroll
+        for (int q = 0; q < 16; q++) o[q] = f32_to_e4m3(y[b + q] * inv);
+        *reinterpret_cast<uint4*>(dst + b) = *reinterpret_cast<const uint4*>(o);
+      }
+      sas[i] = ue8m0_to_float(e);
+    }
   }
   __syncthreads();
   const int nchunks = p.K / 64;
@@ -119,8 +187,8 @@ __global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStr
       ldmatrix_x2(b, xs + (size_t)(lane & 7) * KP + c * 64 + 32 + ((lane >> 3) & 1) * 16);
       mma_e4m3_16832(d1, a, b[0], b[1], d1);
       const float ws = ue8m0_to_float(swr[c >> 1]);
-      const float s0 = 2 * t < p.T ? ws * ue8m0_to_float(p.sA[(size_t)(2 * t) * p.sa_stride + c]) : 0.f;
-      const float s1 = 2 * t + 1 < p.T ? ws * ue8m0_to_float(p.sA[(size_t)(2 * t + 1) * p.sa_stride + c]) : 0.f;
+      const float s0 = ws * sas[(2 * t) * ng + c];
+      const float s1 = ws * sas[(2 * t + 1) * ng + c];
       acc[0] = fmaf(d0[0] + d1[0], s0, acc[0]);
       acc[1] = fmaf(d0[1] + d1[1], s1, acc[1]);
       acc[2] = fmaf(d0[2] + d1[2], s0, acc[2]);
@@ -157,27 +225,40 @@ __global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStr
 using namespace moet;
 
 // Same contract as gemv_fp8 for unbatched weights, T <= 8, K % 64 == 0, K <= 8192.
-void gemv_stream_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tensor sw, torch::Tensor out,
-                     c10::optional<torch::Tensor> resid, torch::Tensor status) {
+void gemv_stream_fp8(c10::optional<torch::Tensor> a_opt, c10::optional<torch::Tensor> sa_opt, torch::Tensor w,
+                     torch::Tensor sw, torch::Tensor out, c10::optional<torch::Tensor> resid, torch::Tensor status,
+                     c10::optional<torch::Tensor> x_norm, c10::optional<torch::Tensor> gamma, double eps) {
+  const bool fuse = x_norm.has_value() && x_norm->defined();
+  const torch::Tensor& a = fuse ? *x_norm : *a_opt;
   const int T = a.size(0), K = w.size(1), N = w.size(0);
   TORCH_CHECK(w.dim() == 2 && w.is_contiguous() && K % 128 == 0 && K <= gs::kMaxK && T <= gs::kMaxT,
               "gemv_stream_fp8: W [N, K] contiguous, K % 128 == 0, K <= 8192, T <= 8");
-  TORCH_CHECK(a.size(1) == K && a.stride(1) == 1 && a.stride(0) % 16 == 0 && sa.stride(1) == 1, "gemv_stream_fp8: A");
+  TORCH_CHECK(a.size(1) == K && a.stride(1) == 1 && (a.stride(0) * a.element_size()) % 16 == 0, "gemv_stream_fp8: A");
+  if (fuse) {
+    TORCH_CHECK(a.scalar_type() == at::kBFloat16 && gamma.has_value() && gamma->numel() == K &&
+                gamma->scalar_type() == at::kBFloat16 && gamma->is_contiguous(),
+                "gemv_stream_fp8: fused norm needs bf16 x and a bf16 gamma of K");
+  } else {
+    TORCH_CHECK(sa_opt.has_value() && sa_opt->stride(1) == 1, "gemv_stream_fp8: activation scales");
+  }
   TORCH_CHECK(reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0,
               "gemv_stream_fp8: 16-byte aligned operands");
   TORCH_CHECK(out.stride(1) == 1 && (out.scalar_type() == at::kFloat || out.scalar_type() == at::kBFloat16),
               "gemv_stream_fp8: out bf16 or f32");
   if (T == 0) return;
   GemvStreamArgs p;
-  p.A = (const uint8_t*)a.data_ptr(); p.sA = (const uint8_t*)sa.data_ptr(); p.a_stride = a.stride(0);
-  p.sa_stride = sa.stride(0);
+  p.A = fuse ? nullptr : (const uint8_t*)a.data_ptr(); p.a_stride = fuse ? 0 : a.stride(0);
+  p.sA = fuse ? nullptr : (const uint8_t*)sa_opt->data_ptr(); p.sa_stride = fuse ? 0 : sa_opt->stride(0);
+  p.xin = fuse ? (const __nv_bfloat16*)a.data_ptr() : nullptr; p.xin_stride = fuse ? a.stride(0) : 0;
+  p.gamma = fuse ? (const __nv_bfloat16*)gamma->data_ptr() : nullptr; p.eps = (float)eps;
   p.W = (const uint8_t*)w.data_ptr(); p.sW = (const uint8_t*)sw.data_ptr(); p.sw_cols = sw.size(1);
   p.out = out.data_ptr(); p.out_stride = out.stride(0); p.out_f32 = out.scalar_type() == at::kFloat;
   p.resid = resid.has_value() && resid->defined() ? (const __nv_bfloat16*)resid->data_ptr() : nullptr;
   if (p.resid) TORCH_CHECK(resid->stride(0) == out.stride(0), "gemv_stream_fp8: resid layout");
   p.T = T; p.N = N; p.K = K; p.status = status.data_ptr<int>();
   const int KP = K + 16;
-  const size_t fixed = (size_t)gs::kMaxT * KP + (size_t)2 * gs::kWarps * gs::kRows * gs::kMaxT * 4 + gs::kMaxRing * 8;
+  const size_t fixed = (size_t)gs::kMaxT * KP + (size_t)2 * gs::kWarps * gs::kRows * gs::kMaxT * 4 +
+                       (size_t)gs::kMaxT * (gs::kMaxK / 64) * 4 + gs::kMaxRing * 8;
   const size_t budget = 220 * 1024;
   const int ring = (int)std::min<size_t>(gs::kMaxRing, (budget - fixed) / ((size_t)gs::kRows * KP));
   TORCH_CHECK(ring >= 2, "gemv_stream_fp8: K too large for a 2-stage ring");

@@ -386,29 +386,31 @@ __global__ void mla_combine_kernel(const float* __restrict__ o_part, const float
 // UE8M0 128x128 block scales) and writes ov[t, h*128 + j] as e4m3 with UE8M0
 // per-64 scales -- the input of the o projection.
 constexpr int kVD = 128, kTC = 16;   // value head dim, tokens per smem chunk
-__global__ void __launch_bounds__(512) mla_combine_uv_kernel(const float* __restrict__ o_part,
+__global__ void __launch_bounds__(256) mla_combine_uv_kernel(const float* __restrict__ o_part,
                                                              const float* __restrict__ ml_part, int S, int T, int Hh,
                                                              const uint8_t* __restrict__ wuv,
                                                              const uint8_t* __restrict__ swuv,
                                                              uint8_t* __restrict__ q, uint8_t* __restrict__ qs) {
   __shared__ __align__(16) float olat[kTC][kLat];
-  __shared__ float ov[kTC][kVD];
+  __shared__ float ov[kTC][kVD / 2];
   __shared__ float wgt[kTC][32];
   __shared__ int nact[kTC];
   const int h = blockIdx.x, TH = T * Hh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint8_t* W = wuv + (size_t)h * kVD * kLat;
   const uint8_t* SW = swuv + (size_t)h * (kLat / 128);
+  // CTA (head h, half hv) computes output rows [64 hv, 64 hv + 64) -- exactly one quantisation group;
   // thread (row j, quarter qk) owns W[j][128*qk .. +128) -- one scale block; immutable, so it is
   // loaded before the dependency wait
-  const int j = threadIdx.x >> 2, qk = threadIdx.x & 3, nwarps = blockDim.x >> 5;
+  const int hv = blockIdx.y;
+  const int jl = threadIdx.x >> 2, j = hv * 64 + jl, qk = threadIdx.x & 3, nwarps = blockDim.x >> 5;
   uint4 wrow[8];
 #pragma unroll
   for (int u = 0; u < 8; u++)
     wrow[u] = __ldg(reinterpret_cast<const uint4*>(W + (size_t)j * kLat + qk * 128) + u);
   const float wsc = ue8m0_to_float(__ldg(SW + qk));
   pdl_entry();
-  const int tbeg = blockIdx.y * kTC, tend = min(T, tbeg + kTC);
+  const int tbeg = blockIdx.z * kTC, tend = min(T, tbeg + kTC);
   for (int t0 = tbeg; t0 < tend; t0 += kTC) {
     const int nt = min(kTC, T - t0);
     // split weights exp2(m_s - M) / sum: one warp per token (S <= 32)
@@ -466,13 +468,13 @@ __global__ void __launch_bounds__(512) mla_combine_uv_kernel(const float* __rest
       float v = acc * wsc;
       v += __shfl_xor_sync(0xffffffffu, v, 1);
       v += __shfl_xor_sync(0xffffffffu, v, 2);
-      if (qk == 0) ov[tt][j] = __bfloat162float(__float2bfloat16(v));
+      if (qk == 0) ov[tt][jl] = __bfloat162float(__float2bfloat16(v));
     }
     __syncthreads();
-    // quantise: one warp per (token, 64-group), 2 values per lane
-    for (int gi = warp; gi < nt * 2; gi += nwarps) {
-      const int tt = gi >> 1, g0 = (gi & 1) * 64;
-      const float a = ov[tt][g0 + 2 * lane], b = ov[tt][g0 + 2 * lane + 1];
+    // quantise: one warp per token (this CTA's 64 outputs form one group), 2 values per lane
+    for (int tt = warp; tt < nt; tt += nwarps) {
+      const int g0 = hv * 64;
+      const float a = ov[tt][2 * lane], b = ov[tt][2 * lane + 1];
       const float amax = warp_max(fmaxf(fabsf(a), fabsf(b)));
       const uint32_t e = ue8m0_for_amax(amax);
       const float inv = (e >= 1 && e <= 253) ? __uint_as_float((254u - e) << 23) : 0.f;
@@ -501,7 +503,7 @@ void mla_combine_uv(torch::Tensor o_part, torch::Tensor ml_part, torch::Tensor w
   TORCH_CHECK(q.is_contiguous() && q.size(-1) * (q.dim() == 3 ? q.size(1) : 1) == (int64_t)Hh * kVD, "mla_combine_uv: out");
   if (T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  launch_k(mla_combine_uv_kernel, dim3(Hh, (T + kTC - 1) / kTC), 512, 0, stream, o_part.data_ptr<float>(), ml_part.data_ptr<float>(), S, T, Hh,
+  launch_k(mla_combine_uv_kernel, dim3(Hh, 2, (T + kTC - 1) / kTC), 256, 0, stream, o_part.data_ptr<float>(), ml_part.data_ptr<float>(), S, T, Hh,
            (const uint8_t*)wuv.data_ptr(), (const uint8_t*)swuv.data_ptr(), (uint8_t*)q.data_ptr(),
            (uint8_t*)qs.data_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -280,12 +280,13 @@ __global__ void build_pairs_kernel(const int* __restrict__ topk_ids, int R, int 
   build_pairs_block(topk_ids, R, k, E, MB, rank_scratch, sorted_tok, pos_of, pairs, n_pairs, status, pad, n_rows);
 }
 
-// Decode routing in one launch: every CTA computes the router logits of 16
-// experts for all T tokens (bf16 x and W, fp32 sums; the weights are
-// prefetched before the dependency wait); the last CTA to finish (arrival
-// counter, self-resetting) runs the top-k of every token and builds the
-// expert pair list.
+// Decode routing in one launch: every CTA computes the router logits of 4
+// experts for all T tokens (4 warps per expert, each over a quarter of H;
+// bf16 x and W, fp32 sums; the weight rows are loaded before the dependency
+// wait); the last CTA to finish (arrival counter, self-resetting) runs the
+// top-k of every token and builds the expert pair list.
 constexpr int kRouteWarps = 16;
+constexpr int kRouteExperts = 4;
 __global__ void __launch_bounds__(kRouteWarps * 32) moe_route_fused_kernel(
     const __nv_bfloat16* __restrict__ x, int T, int H, const __nv_bfloat16* __restrict__ w, int E,
     float* __restrict__ logits, const float* __restrict__ bias, int k, int sigmoid, int n_group, int topk_group,
@@ -293,53 +294,58 @@ __global__ void __launch_bounds__(kRouteWarps * 32) moe_route_fused_kernel(
     int* __restrict__ rank_scratch, int* __restrict__ sorted_tok, int* __restrict__ pos_of,
     int4* __restrict__ pairs, int* __restrict__ n_pairs, int* __restrict__ counter, int* __restrict__ status) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x * kRouteWarps + warp;
-  // The expert's weight row is immutable: its first 16 x 16 B per lane (H <= 4096
-  // entirely) go to registers before the dependency wait.
-  constexpr int kPre = 16;
-  const int nvec = H / 256;   // 16-byte vectors per lane
-  const __nv_bfloat16* wr = w + (size_t)min(e, E - 1) * H;
+  const int el = warp >> 2, qh = warp & 3;
+  const int e = blockIdx.x * kRouteExperts + el;
+  const int Hq = H >> 2, h0 = qh * Hq;
+  constexpr int kPre = 8;
+  const int nvec = Hq / 256;      // 16-byte vectors per lane in this quarter
+  const __nv_bfloat16* wr = w + (size_t)min(e, E - 1) * H + h0;
   uint4 wv[kPre];
 #pragma unroll
   for (int u = 0; u < kPre; u++)
     if (u < nvec) wv[u] = __ldg(reinterpret_cast<const uint4*>(wr + u * 256 + lane * 8));
   pdl_entry();
-  // tokens are staged through shared memory 4 at a time (all loads in flight at once)
   extern __shared__ __align__(16) uint8_t route_smem[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(route_smem);   // [4][H]
+  __shared__ float qpart[kRouteWarps][4];
   for (int t0 = 0; t0 < T; t0 += 4) {
     const int nt = min(4, T - t0);
     __syncthreads();
     for (int i = threadIdx.x; i < nt * H / 8; i += blockDim.x)
       reinterpret_cast<uint4*>(xs)[i] = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t0 * H) + i);
     __syncthreads();
-    if (e < E) {
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int u0 = 0; u0 < nvec; u0 += kPre) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int u0 = 0; u0 < nvec; u0 += kPre) {
 #pragma unroll
-        for (int u = 0; u < kPre; u++) {
-          if (u0 + u >= nvec) break;
-          const uint4 wq = u0 == 0 ? wv[u] : __ldg(reinterpret_cast<const uint4*>(wr + (u0 + u) * 256 + lane * 8));
-          const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wq);
+      for (int u = 0; u < kPre; u++) {
+        if (u0 + u >= nvec) break;
+        const uint4 wq = u0 == 0 ? wv[u] : __ldg(reinterpret_cast<const uint4*>(wr + (u0 + u) * 256 + lane * 8));
+        const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wq);
 #pragma unroll
-          for (int j = 0; j < 4; j++) {
-            if (j < nt) {
-              const uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)j * H + (u0 + u) * 256 + lane * 8);
-              const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
+        for (int j = 0; j < 4; j++) {
+          if (j < nt) {
+            const uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)j * H + h0 + (u0 + u) * 256 + lane * 8);
+            const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
 #pragma unroll
-              for (int i = 0; i < 4; i++) {
-                const float2 a = __bfloat1622float2(x2[i]), b = __bfloat1622float2(w2[i]);
-                acc[j] = fmaf(a.x, b.x, fmaf(a.y, b.y, acc[j]));
-              }
+            for (int i = 0; i < 4; i++) {
+              const float2 a = __bfloat1622float2(x2[i]), b = __bfloat1622float2(w2[i]);
+              acc[j] = fmaf(a.x, b.x, fmaf(a.y, b.y, acc[j]));
             }
           }
         }
       }
+    }
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const float v = warp_sum(acc[j]);
-        if (lane == 0 && j < nt) logits[(size_t)(t0 + j) * E + e] = v;
-      }
+    for (int j = 0; j < 4; j++) {
+      const float v = warp_sum(acc[j]);
+      if (lane == 0) qpart[warp][j] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < kRouteExperts * 4) {      // (expert, token) -> sum of the 4 quarters in fixed order
+      const int ee = threadIdx.x >> 2, j = threadIdx.x & 3, eg = blockIdx.x * kRouteExperts + ee;
+      if (eg < E && j < nt)
+        logits[(size_t)(t0 + j) * E + eg] = ((qpart[ee * 4][j] + qpart[ee * 4 + 1][j]) + qpart[ee * 4 + 2][j]) +
+                                            qpart[ee * 4 + 3][j];
     }
   }
   __shared__ int last;
@@ -418,7 +424,7 @@ void moe_route_fused(torch::Tensor x, torch::Tensor w, torch::Tensor logits, c10
                      torch::Tensor counter, torch::Tensor status) {
   const int T = x.size(0), H = x.size(1), E = w.size(0);
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.is_contiguous() &&
-              w.is_contiguous() && H % 256 == 0, "moe_route_fused: bf16 contiguous, H % 256 == 0");
+              w.is_contiguous() && H % 1024 == 0, "moe_route_fused: bf16 contiguous, H % 1024 == 0");
   TORCH_CHECK(E <= kRouteWarps * 32 && k <= 32 && n_group <= 64, "moe_route_fused: E <= 512, k <= 32");
   TORCH_CHECK(pairs.size(0) >= (int64_t)T * k / MB + std::min<int64_t>(E, (int64_t)T * k), "moe_route_fused: pairs");
   if (T == 0) return;
@@ -426,7 +432,7 @@ void moe_route_fused(torch::Tensor x, torch::Tensor w, torch::Tensor logits, c10
   const size_t smem = (size_t)4 * H * 2;
   // static shared memory of the top-k / pair-list phases + the token stage exceed the 48 KiB default
   cudaFuncSetAttribute(moe_route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  launch_k(moe_route_fused_kernel, (E + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, smem, stream,
+  launch_k(moe_route_fused_kernel, (E + kRouteExperts - 1) / kRouteExperts, kRouteWarps * 32, smem, stream,
            (const __nv_bfloat16*)x.data_ptr(), T, H, (const __nv_bfloat16*)w.data_ptr(), E, logits.data_ptr<float>(),
            bias.has_value() && bias->defined() ? (const float*)bias->data_ptr<float>() : (const float*)nullptr,
            (int)k, sigmoid ? 1 : 0, (int)n_group, (int)topk_group, norm ? 1 : 0, (float)scaling,

@@ -606,3 +606,23 @@ def test_gemv_stream_matches_gemv(C, T, N, K):
     ob = torch.empty(T, N, dtype=torch.bfloat16, device=DEV)
     C.gemv_stream_fp8(aq, sa, w, sw, ob, resid, st)
     assert torch.allclose(ob.float(), (ref + resid.float()), rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("T,N,K", [(3, 1600, 4096), (1, 6144, 1024), (8, 512, 2048)])
+def test_gemv_stream_fused_norm(C, T, N, K):
+    """RMSNorm + e4m3 quantisation in the GEMV prologue equals rmsnorm_quant followed by the GEMV."""
+    g = torch.Generator().manual_seed(T * N)
+    from vllm_moet_b200.models.weights import Fp8Linear
+    lin = Fp8Linear.from_float(torch.randn(N, K, generator=g) * 0.05)
+    w, sw = lin.w.to(DEV), lin.s.to(DEV)
+    x = (torch.randn(T, K + 64, generator=g) * 2).to(torch.bfloat16).to(DEV)[:, :K]   # strided rows
+    gamma = (torch.rand(K, generator=g) + 0.5).to(torch.bfloat16).to(DEV)
+    q = torch.empty(T, K, dtype=torch.uint8, device=DEV); s = torch.empty(T, K // 64, dtype=torch.uint8, device=DEV)
+    C.rmsnorm_quant(x, None, None, gamma, 1e-6, None, q, s, None, None, 0)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ref = torch.empty(T, N, device=DEV)
+    C.gemv_stream_fp8(q, s, w, sw, ref, None, st)
+    out = torch.empty(T, N, device=DEV)
+    C.gemv_stream_fp8(None, None, w, sw, out, None, st, x, gamma, 1e-6)
+    assert int(st) == 0
+    assert torch.allclose(out, ref, rtol=1e-4, atol=1e-3), float((out - ref).abs().max())

@@ -300,18 +300,31 @@ class NativeRunner:
         cfg, C, T, Hh = self.cfg, self.C, ctx.T, self.Hh
         H, ql, lat, rope, nope, vd = cfg.hidden, cfg.q_lora_rank, cfg.kv_lora_rank, cfg.qk_rope_dim, cfg.qk_nope_dim, cfg.v_head_dim
         hq, hs = self._fp8("h", T, H)
-        self._norm_in(x, lw.attn_norm, None, hq, hs)
         qkva = self.ws.get("qkva", (T, ql + lat + rope), torch.bfloat16)
-        self._gemv(hq, hs, lw.qkv_a, qkva)
         qaq, qas = self._fp8("qa", T, ql)
         ovq, ovs = self._fp8("ov", T, Hh * vd)
+        qb = self.ws.get("qb", (T, Hh * (nope + rope)), torch.bfloat16)
+        # decode: the input norms are fused into the streaming GEMVs' prologues (no separate
+        # RMSNorm launches); needs no pending TP reduction and no indexer (which reads hq / qa)
+        fuse = (ctx.mode == "decode" and T <= 8 and self.gemv_stream and self._pend is None
+                and lw.idx_wq is None and isinstance(lw.qkv_a.w, torch.Tensor) and lw.qkv_a.w.dim() == 2
+                and H % 128 == 0 and ql % 128 == 0 and H <= 6144 and ql <= 6144)
+        if fuse:
+            C.gemv_stream_fp8(None, None, lw.qkv_a.w, lw.qkv_a.s, qkva, None, self.status, x, lw.attn_norm,
+                              cfg.rms_eps)
+        else:
+            self._norm_in(x, lw.attn_norm, None, hq, hs)
+            self._gemv(hq, hs, lw.qkv_a, qkva)
         if ctx.mode == "decode":
             with self._fork():     # latent KV path (norm, rope, cache write) beside the query path
                 C.kv_prep(qkva[:, ql:], lat, rope, lw.kv_a_norm, cfg.rms_eps, ctx.pos, self.cos_sin, ctx.slot,
                           self.kv_mode, cache, None, None, None, None, self.status)
-        C.rmsnorm_quant(qkva[:, :ql], None, None, lw.q_a_norm, cfg.rms_eps, None, qaq, qas, None, None, 0)
-        qb = self.ws.get("qb", (T, Hh * (nope + rope)), torch.bfloat16)
-        self._gemv(qaq, qas, lw.q_b, qb)
+        if fuse:
+            C.gemv_stream_fp8(None, None, lw.q_b.w, lw.q_b.s, qb, None, self.status, qkva[:, :ql], lw.q_a_norm,
+                              cfg.rms_eps)
+        else:
+            C.rmsnorm_quant(qkva[:, :ql], None, None, lw.q_a_norm, cfg.rms_eps, None, qaq, qas, None, None, 0)
+            self._gemv(qaq, qas, lw.q_b, qb)
         sel = self._indexer(lw, hq, hs, qaq, qas, ctx, li) if lw.idx_wq is not None else None
         if ctx.mode == "decode":
             qnq = self.ws.get("qn.q", (T, Hh, nope), torch.uint8)
@@ -400,7 +413,7 @@ class NativeRunner:
         L = ex.layout
         I = L.I
         use_tc = ctx.mode == "prefill" and H % 128 == 0 and I % 128 == 0 and (2 * I) % 128 == 0
-        if T <= 64 and not use_tc:
+        if T <= 64 and not use_tc and H % 1024 == 0:
             # decode: logits + top-k + pair list in one launch
             MB = ctx.mb
             P = R // MB + min(E, R)
