@@ -43,7 +43,8 @@ void gather_rows(torch::Tensor src_q, torch::Tensor src_s, torch::Tensor idx, to
 void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor> gather, torch::Tensor pairs,
                  torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
                  torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
-                 c10::optional<torch::Tensor> miss_count);
+                 c10::optional<torch::Tensor> miss_count, c10::optional<torch::Tensor> pool8, int64_t codes_off8,
+                 int64_t scale_off8, c10::optional<torch::Tensor> slot_table8);
 void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::optional<torch::Tensor> resid,
                  c10::optional<torch::Tensor> shared_out, c10::optional<torch::Tensor> out,
                  c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> ar);
@@ -144,7 +145,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax_split", &argmax_split, py::arg("logits"), py::arg("ids"), py::arg("lse"), py::arg("status"),
         py::arg("part"), py::arg("counter"), py::arg("mv") = py::none(), py::arg("id_offset") = 0);
   m.def("argmax_merge", &argmax_merge);
-  m.def("moe_w2_gemv", &moe_w2_gemv);
+  m.def("moe_w2_gemv", &moe_w2_gemv, py::arg("a"), py::arg("sa"), py::arg("gather"), py::arg("pairs"),
+        py::arg("n_pairs"), py::arg("pool"), py::arg("codes_off"), py::arg("scale_off"), py::arg("slot_table"),
+        py::arg("out"), py::arg("N"), py::arg("K"), py::arg("rows_per_pair"), py::arg("miss_count"),
+        py::arg("pool8") = py::none(), py::arg("codes_off8") = 0, py::arg("scale_off8") = 0,
+        py::arg("slot_table8") = py::none());
   m.def("moe_combine", &moe_combine, py::arg("y"), py::arg("pos_of"), py::arg("wts"), py::arg("resid"),
         py::arg("shared_out"), py::arg("out"), py::arg("out_f32"), py::arg("ar") = py::none());
   m.def("bf12_decode", &bf12_decode);

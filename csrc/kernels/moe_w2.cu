@@ -34,6 +34,10 @@ struct W2Args {
   float* out; long long out_stride;
   int N, K;
   int* miss_count;
+  // FP4 delta tier (direct-8 planes: e4m3 bytes in A-fragment order + UE8M0 block-32
+  // scales); an expert with a delta slot >= 0 is served from it instead of the 2-bit slot
+  const uint8_t* pool8; long long slot_bytes8, codes_off8, scale_off8;
+  const int* slot_table8;
 };
 
 template <int NT>
@@ -46,7 +50,8 @@ __global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Arg
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int nb = blockIdx.x * (blockDim.x >> 5) + warp;  // 16-row block
   if (nb * 16 >= p.N) return;
-  const int slot = p.slot_table[e];
+  const int slot8 = p.slot_table8 ? p.slot_table8[e] : -1;
+  const int slot = slot8 >= 0 ? slot8 : p.slot_table[e];
   if (slot < 0) {
     if (blockIdx.x == 0 && threadIdx.x == 0 && p.miss_count) atomicAdd(p.miss_count, 1);
     for (int j = 0; j < nrows; j++)
@@ -54,9 +59,11 @@ __global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Arg
     return;
   }
   const int KC = p.K >> 6, KS = p.K >> 5;
-  const uint8_t* base = p.pool + (size_t)slot * p.slot_bytes;
-  const uint8_t* codes = base + p.codes_off + (size_t)nb * KC * 256 + lane * 8;
-  const uint8_t* sc = base + p.scale_off + (size_t)nb * KS * 16;
+  const bool direct = slot8 >= 0;
+  const uint8_t* base = direct ? p.pool8 + (size_t)slot8 * p.slot_bytes8 : p.pool + (size_t)slot * p.slot_bytes;
+  const uint8_t* codes = direct ? base + p.codes_off8 + (size_t)nb * KC * 1024 + lane * 32
+                                : base + p.codes_off + (size_t)nb * KC * 256 + lane * 8;
+  const uint8_t* sc = base + (direct ? p.scale_off8 : p.scale_off) + (size_t)nb * KS * 16;
 
   // activation row of sorted row r0 + j (gathered through the token map for w13)
   auto act_row = [&](int j) -> int {
@@ -89,6 +96,48 @@ __global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Arg
   // fragment and the two block scales are applied with FMAs.
   constexpr uint32_t L = 0x4838B8C8u;   // e4m3 {-4, -1, +1, +4}
   constexpr int U = 8;
+  auto mma_chunk = [&](int c, const uint32_t (&A0)[4], const uint32_t (&A1)[4]) {
+    const uint8_t* s = ss + c * 32;
+    const float sga = ue8m0_to_float(s[g]), sha = ue8m0_to_float(s[g + 8]);
+    const float sgb = ue8m0_to_float(s[16 + g]), shb = ue8m0_to_float(s[24 + g]);
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+      uint2 xa = make_uint2(0, 0), xb = make_uint2(0, 0);
+      if (xr[nt] >= 0) {
+        const uint8_t* xp = xbase + (size_t)xr[nt] * p.a_stride + (size_t)c * 64;
+        xa = __ldg(reinterpret_cast<const uint2*>(xp));
+        xb = __ldg(reinterpret_cast<const uint2*>(xp + 32));
+      }
+      float da[4] = {0.f, 0.f, 0.f, 0.f}, db[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_e4m3_16832(da, A0, xa.x, xa.y, da);
+      mma_e4m3_16832(db, A1, xb.x, xb.y, db);
+      const float as0 = sr0[nt] >= 0 ? ue8m0_to_float(__ldg(p.sA + (size_t)sr0[nt] * KC64 + c)) : 0.f;
+      const float as1 = sr1[nt] >= 0 ? ue8m0_to_float(__ldg(p.sA + (size_t)sr1[nt] * KC64 + c)) : 0.f;
+      acc[nt][0] = fmaf(fmaf(da[0], sga, db[0] * sgb), as0, acc[nt][0]);
+      acc[nt][1] = fmaf(fmaf(da[1], sga, db[1] * sgb), as1, acc[nt][1]);
+      acc[nt][2] = fmaf(fmaf(da[2], sha, db[2] * shb), as0, acc[nt][2]);
+      acc[nt][3] = fmaf(fmaf(da[3], sha, db[3] * shb), as1, acc[nt][3]);
+    }
+  };
+  if (direct) {     // delta tier: the A-fragments are stored as e4m3 bytes, no decode
+    constexpr int UD = 2;
+    for (int c0 = 0; c0 < KC; c0 += UD) {
+      uint4 w0[UD], w1[UD];
+#pragma unroll
+      for (int u = 0; u < UD; u++)
+        if (c0 + u < KC) {
+          w0[u] = ldg_stream_u4(codes + (size_t)(c0 + u) * 1024);
+          w1[u] = ldg_stream_u4(codes + (size_t)(c0 + u) * 1024 + 16);
+        }
+#pragma unroll
+      for (int u = 0; u < UD; u++) {
+        if (c0 + u >= KC) break;
+        const uint32_t A0[4] = {w0[u].x, w0[u].y, w0[u].z, w0[u].w};
+        const uint32_t A1[4] = {w1[u].x, w1[u].y, w1[u].z, w1[u].w};
+        mma_chunk(c0 + u, A0, A1);
+      }
+    }
+  } else
   for (int c0 = 0; c0 < KC; c0 += U) {
     uint2 wv[U];
 #pragma unroll
@@ -200,7 +249,8 @@ using namespace moet;
 void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor> gather, torch::Tensor pairs,
                  torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
                  torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
-                 c10::optional<torch::Tensor> miss_count) {
+                 c10::optional<torch::Tensor> miss_count, c10::optional<torch::Tensor> pool8, int64_t codes_off8,
+                 int64_t scale_off8, c10::optional<torch::Tensor> slot_table8) {
   TORCH_CHECK(K % 64 == 0 && N % 16 == 0, "moe_w2_gemv: N % 16, K % 64");
   TORCH_CHECK(a.stride(1) == 1 && a.size(1) == K, "moe_w2_gemv: A [rows, K] inner-contiguous");
   TORCH_CHECK(sa.is_contiguous() && sa.size(1) == K / 64, "moe_w2_gemv: sA [rows, K/64]");
@@ -217,6 +267,13 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
   p.out = out.data_ptr<float>(); p.out_stride = out.stride(0);
   p.N = N; p.K = K;
   p.miss_count = miss_count.has_value() && miss_count->defined() ? miss_count->data_ptr<int>() : nullptr;
+  p.pool8 = nullptr; p.slot_table8 = nullptr; p.slot_bytes8 = p.codes_off8 = p.scale_off8 = 0;
+  if (pool8.has_value() && pool8->defined()) {
+    TORCH_CHECK(slot_table8.has_value() && pool8->dim() == 2 && pool8->stride(0) % 16 == 0 && codes_off8 % 16 == 0 &&
+                scale_off8 % 16 == 0, "moe_w2_gemv: delta pool [slots, bytes] with a slot table, 16-byte aligned");
+    p.pool8 = (const uint8_t*)pool8->data_ptr(); p.slot_bytes8 = pool8->stride(0);
+    p.codes_off8 = codes_off8; p.scale_off8 = scale_off8; p.slot_table8 = slot_table8->data_ptr<int>();
+  }
   const int max_pairs = pairs.size(0);
   const int wpc = 4;
   dim3 grid((N / 16 + wpc - 1) / wpc, max_pairs);

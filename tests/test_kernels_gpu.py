@@ -626,3 +626,50 @@ def test_gemv_stream_fused_norm(C, T, N, K):
     C.gemv_stream_fp8(None, None, w, sw, out, None, st, x, gamma, 1e-6)
     assert int(st) == 0
     assert torch.allclose(out, ref, rtol=1e-4, atol=1e-3), float((out - ref).abs().max())
+
+
+def test_moe_gemv_delta_tier(C):
+    """Experts with a delta slot are read from the direct-8 FP4 plane (MXFP4 values),
+    the rest from the 2-bit base; both match their dequantised references."""
+    from vllm_moet_b200.residency.delta import delta_layout, pack_delta_slot, dequant_delta_slot
+    g = torch.Generator().manual_seed(5)
+    E, H, I, T, k, MB = 6, 256, 128, 3, 2, 8
+    w13 = torch.randn(E, 2 * I, H, generator=g) * 0.05
+    w2 = torch.randn(E, H, I, generator=g) * 0.05
+    from vllm_moet_b200.models.weights import ExpertLayout, quantize_experts_cpu
+    lay = ExpertLayout(H=H, I=I)
+    pool = torch.empty(E, lay.slot_bytes, dtype=torch.uint8)
+    quantize_experts_cpu(w13, w2, lay, pool)
+    sb8 = delta_layout(H, I)[0]
+    rows8 = torch.stack([pack_delta_slot(w13[e], w2[e]) for e in range(E)])
+    pool8 = torch.zeros(2, sb8, dtype=torch.uint8)
+    table8 = torch.full((E,), -1, dtype=torch.int32)
+    pool8[0], table8[1] = rows8[1], 0
+    pool8[1], table8[4] = rows8[4], 1
+    ids = torch.tensor([[1, 2], [4, 1], [0, 5]], dtype=torch.int32)
+    R = T * k
+    P = R // MB + min(E, R)
+    rank = torch.empty(R, dtype=torch.int32, device=DEV); stok = torch.empty(R, dtype=torch.int32, device=DEV)
+    posof = torch.empty(R, dtype=torch.int32, device=DEV); pairs = torch.empty(P, 4, dtype=torch.int32, device=DEV)
+    npairs = torch.empty(1, dtype=torch.int32, device=DEV); st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    C.build_pairs(ids.to(DEV), E, MB, rank, stok, posof, pairs, npairs, st)
+    x = torch.randn(T, H, generator=g)
+    q, s = fp8.quant_act_fp8(x)
+    qw = fp8.to_w2_layout(q.view(torch.uint8)).to(DEV)
+    out = torch.empty(R, 2 * I, device=DEV)
+    o13 = delta_layout(H, I)
+    C.moe_w2_gemv(qw, s.to(DEV), stok, pairs, npairs, pool.to(DEV), lay.off_codes13, lay.off_sc13,
+                  torch.arange(E, dtype=torch.int32, device=DEV), out, 2 * I, H, MB, None,
+                  pool8=pool8.to(DEV), codes_off8=o13[1], scale_off8=o13[2], slot_table8=table8.to(DEV))
+    A = fp8.dequant_act_fp8(q, s).double()
+    po = posof.cpu().long()
+    from vllm_moet_b200.formats import planes as pl
+    for t in range(T):
+        for j in range(k):
+            e = int(ids[t, j])
+            if int(table8[e]) >= 0:
+                W = dequant_delta_slot(rows8[e], H, I)[0].double()
+            else:
+                c13, s13, _, _ = lay.split(pool[e])
+                W = pl.dequant_plane(c13, s13, 2 * I, H).double()
+            assert rel(out[po[t * k + j]].cpu(), A[t] @ W.t()) < 1e-4, (t, j, e)

@@ -41,3 +41,39 @@ def test_cached_experts_match_resident(resident_tokens, kind, tmp_path):
     assert st["fetched_rows"] > 0
     assert llm.replay.stats["steps"] > 0
     llm.cache.close()
+
+
+def test_delta_tier_and_gate(resident_tokens):
+    """Gate never firing: tokens equal the base engine.  Gate always firing with a pool
+    that holds every expert: every decode step replays on FP4 experts, and the
+    tokens track an oracle whose experts are the FP4 (MXFP4) weights."""
+    from vllm_moet_b200.models import reference
+    from vllm_moet_b200.residency.delta import dequant_delta_slot
+    quiet = LLM(_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=512, max_num_seqs=2,
+                delta_slots=48, gate=True)
+    quiet.gate.tau = -1.0           # never fires
+    out = [o.outputs[0].token_ids for o in quiet.generate(_prompts(), SamplingParams(max_tokens=12, ignore_eos=True))]
+    assert out == resident_tokens
+    del quiet
+    torch.cuda.empty_cache()
+    loud = LLM(_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=512, max_num_seqs=2,
+               delta_slots=48, gate=True)
+    loud.gate.tau = 2.0             # always fires (max-prob <= 1)
+    p = _prompts()[0]
+    toks = loud.generate([p], SamplingParams(max_tokens=6, ignore_eos=True))[0].outputs[0].token_ids
+    assert loud.delta.stats["gate_replays"] > 0 and loud.delta.stats["fetched_rows"] > 0
+    # oracle over FP4 experts for the decode part (the first token comes from prefill on the base)
+    from vllm_moet_b200.residency import moe_layers
+    lay = moe_layers(loud.mw)[0].experts.layout
+    for li, lw in enumerate(moe_layers(loud.mw)):
+        rows = loud.delta.store.layers[li]
+        d = [dequant_delta_slot(rows[e].cpu(), lay.H, lay.I) for e in range(rows.shape[0])]
+        lw.experts.dense_w13 = torch.stack([a for a, _ in d]).cuda()
+        lw.experts.dense_w2 = torch.stack([b for _, b in d]).cuda()
+    cs = reference.rope_cos_sin(loud.cfg, 256, "cuda")
+    seq = list(p) + [toks[0]]
+    for tok in toks[1:]:
+        lg, _ = reference.forward(loud.mw, torch.tensor(seq, device="cuda"), torch.arange(len(seq), device="cuda"), cs)
+        row = lg[-1]
+        assert float(row[tok]) >= float(row.max()) - 0.5 * (float(row.std()) + 1e-6), (tok, int(row.argmax()))
+        seq.append(tok)

@@ -112,6 +112,7 @@ class NativeRunner:
         self.tp_rank, self.tp_size = mw.tp_rank, mw.tp_size
         self.ar = None            # fused peer-memory all-reduce (SymmAllReduce) for decode-sized steps
         self.cache = None         # residency.ExpertCache when routed experts are served from a host store
+        self.delta = None         # residency.DeltaTier (FP4 hot experts) when enabled
         self._moe_index = {}
         self._pend = None         # (residual, out) of a pushed reduction the next RMSNorm completes
         self._fused = False
@@ -213,6 +214,17 @@ class NativeRunner:
         self.cache = cache
         self.miss = cache.miss_count
         self._moe_index = {id(lw): i for i, lw in enumerate(moe_layers(self.mw))}
+
+    def attach_delta_tier(self, tier):
+        """Serve experts that hold a delta slot at FP4 precision (decode GEMVs)."""
+        from ..residency import moe_layers
+        self.delta = tier
+        if not self._moe_index:
+            self._moe_index = {id(lw): i for i, lw in enumerate(moe_layers(self.mw))}
+
+    def main_logits(self, B: int):
+        """Logits [B*(1+k), V] of the last decode step of bucket B (verify rows)."""
+        return self._bucket_ws(B).bufs.get(("main.logits", torch.float32))
 
     def route_ids(self, B: int):
         """Per-MoE-layer routed expert ids of the last decode step of bucket B."""
@@ -427,7 +439,7 @@ class NativeRunner:
                               cfg.n_group, cfg.topk_group, cfg.norm_topk_prob, cfg.routed_scaling, ids, wts, MB,
                               rank, stok, posof, pairs, npairs, cnt, self.status)
             self._ensure_experts(mli, ids)
-            y2 = self._moe_gemv_pairs(h2q, h2s, stok, pairs, npairs, ex, R, MB)
+            y2 = self._moe_gemv_pairs(h2q, h2s, stok, pairs, npairs, ex, R, MB, mli)
         else:
             if T <= 64:
                 C.router_logits(hb, self._router_w(lw), logits)
@@ -439,7 +451,7 @@ class NativeRunner:
             if use_tc:
                 y2, posof = self._moe_tc(h2q, h2s, ids, ex, R, T)
             else:
-                y2, posof = self._moe_gemv(h2q, h2s, ids, ex, R, ctx.mb)
+                y2, posof = self._moe_gemv(h2q, h2s, ids, ex, R, ctx.mb, mli)
         if sh is not None:
             self._join()
         if self.tp_group is None:
@@ -484,7 +496,7 @@ class NativeRunner:
                     self.miss, self.status, None)
         return y2, posof
 
-    def _moe_gemv(self, h2q, h2s, ids, ex, R, MB):
+    def _moe_gemv(self, h2q, h2s, ids, ex, R, MB, mli=None):
         """Decode experts: mma.sync weight-streaming GEMV over the compact pair list."""
         C, cfg = self.C, self.cfg
         E, H = cfg.num_experts, cfg.hidden
@@ -497,21 +509,27 @@ class NativeRunner:
         pairs = self.ws.get("pairs", (P, 4), torch.int32)
         npairs = self.ws.get("npairs", (1,), torch.int32)
         C.build_pairs(ids, E, MB, rank, stok, posof, pairs, npairs, self.status)
-        return self._moe_gemv_pairs(h2q, h2s, stok, pairs, npairs, ex, R, MB), posof
+        return self._moe_gemv_pairs(h2q, h2s, stok, pairs, npairs, ex, R, MB, mli), posof
 
-    def _moe_gemv_pairs(self, h2q, h2s, stok, pairs, npairs, ex, R, MB):
+    def _moe_gemv_pairs(self, h2q, h2s, stok, pairs, npairs, ex, R, MB, mli=None):
         C, cfg = self.C, self.cfg
         H = cfg.hidden
         L = ex.layout
         I = L.I
+        d13 = d2 = {}
+        if self.delta is not None and mli is not None:    # FP4 delta slots first, 2-bit base otherwise
+            o13, os13, o2, os2 = self.delta.offsets
+            t8 = self.delta.slot_table[mli]
+            d13 = dict(pool8=self.delta.pool, codes_off8=o13, scale_off8=os13, slot_table8=t8)
+            d2 = dict(pool8=self.delta.pool, codes_off8=o2, scale_off8=os2, slot_table8=t8)
         c13 = self.ws.get("c13", (R, 2 * I), torch.float32)
         C.moe_w2_gemv(h2q, h2s, stok, pairs, npairs, ex.pool, L.off_codes13, L.off_sc13, ex.slot_table, c13,
-                      2 * I, H, MB, self.miss)
+                      2 * I, H, MB, self.miss, **d13)
         a2q, a2s = self._fp8("a2", R, I)
         C.swiglu_quant(c13, cfg.swiglu_limit or 0.0, None, 1, a2q, a2s)
         y2 = self.ws.get("y2", (R, H), torch.float32)
         C.moe_w2_gemv(a2q, a2s, None, pairs, npairs, ex.pool, L.off_codes2, L.off_sc2, ex.slot_table, y2,
-                      H, I, MB, self.miss)
+                      H, I, MB, self.miss, **d2)
         return y2
 
     def _check(self, name, t):

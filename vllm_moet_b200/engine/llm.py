@@ -46,6 +46,7 @@ class LLM:
                  num_layers: Optional[int] = None, cuda_graphs: bool = True, num_gpu_blocks: Optional[int] = None,
                  tensor_parallel_size: int = 1, tp_group=None, tp_rank: int = 0,
                  pipeline_parallel_size: int = 1, pp_group=None, pp_rank: int = 0, expert_cache_slots: int = 0,
+                 delta_slots: int = 0, gate: Optional[bool] = None,
                  expert_store: str = "pinned", expert_store_dir: Optional[str] = None, **model_overrides):
         cfg = get_preset(model, **model_overrides) if isinstance(model, str) else model
         if num_layers is not None:
@@ -66,7 +67,8 @@ class LLM:
         self.tokenizer = ByteTokenizer(cfg.vocab)
         self.mw = weights if weights is not None else random_weights(
             cfg, self.device, seed=seed, tp_rank=tp_rank, tp_size=tensor_parallel_size,
-            with_mtp=num_speculative_tokens > 0, pp_rank=pp_rank, pp_size=pipeline_parallel_size)
+            with_mtp=num_speculative_tokens > 0, pp_rank=pp_rank, pp_size=pipeline_parallel_size,
+            with_delta=bool(delta_slots) and self.device.type == "cuda")
         if pipeline_parallel_size > 1:
             # MTP presence is a property of the model, known on every stage
             self._has_mtp = num_speculative_tokens > 0 and cfg.num_mtp_layers > 0
@@ -94,6 +96,9 @@ class LLM:
                 slots = int(self.ecfg.moet.base_cache_gb * (1 << 30) // sb)
             if slots:
                 self._attach_cache(slots, expert_store, expert_store_dir, tp_group)
+            self.delta = self.gate = None
+            if delta_slots:
+                self._attach_delta(delta_slots, gate)
             self._DecodeState = DecodeState
             self._states = {}
             self._pin_active = None
@@ -101,6 +106,34 @@ class LLM:
             from .torch_runner import TorchRunner
             self.blocks = None
             self.runner = TorchRunner(self.mw, self.k, max_model_len, self.device)
+
+    def _attach_delta(self, slots, gate):
+        """FP4 delta tier of `slots` hot experts (+ the confidence gate that fills it)."""
+        from ..residency import ConfidenceGate, moe_layers
+        from ..residency.delta import DeltaTier
+        m = self.ecfg.moet
+        layers = moe_layers(self.mw)
+        rows = [lw.experts.delta_rows for lw in layers]
+        if any(r is None for r in rows):
+            raise ValueError("delta tier needs weights built with delta rows")
+        lay = layers[0].experts.layout
+        self.delta = DeltaTier(rows, lay.H, lay.I, slots, device=self.device, policy=m.delta_policy,
+                               decay=m.delta_decay)
+        for lw in layers:
+            lw.experts.delta_rows = None
+        self.runner.attach_delta_tier(self.delta)
+        if gate if gate is not None else m.gate:
+            self.gate = ConfidenceGate(tau=m.gate_tau, signal=m.gate_signal, agg=m.gate_agg, fp_max=m.gate_fp_max,
+                                       max_promote=m.gate_max_promote)
+            self.ecfg.cuda_graphs = self.ecfg.cuda_graphs  # gate replays reuse the captured graph
+
+    def _routed_pairs(self, B):
+        ids = self.runner.route_ids(B)
+        pairs = []
+        for li, t in enumerate(ids):
+            if t is not None:
+                pairs += [(li, int(e)) for e in torch.unique(t).tolist()]
+        return pairs
 
     def _attach_cache(self, slots, kind, store_dir, tp_group):
         """Routed experts from a host store through a GPU expert cache of `slots` slots,
@@ -266,6 +299,8 @@ class LLM:
             if self.ecfg.cuda_graphs and graph is None:
                 graph = runner.capture(st)
             t0 = time.perf_counter()
+            if self.delta is not None:
+                self._delta_snap = st.snapshot()
             if self.cache is not None:
                 self.cache.wait_idle()           # safe point: no pool / slot-table mutation in flight
                 self.cache.step_begin()
@@ -280,6 +315,8 @@ class LLM:
                 graph.replay()
             else:
                 runner.decode_body(st)
+            if self.delta is not None:
+                self._delta_step(st, B, graph, kp1)
             pin_out.copy_(st.out_tokens, non_blocking=True)
             pin_acc.copy_(st.n_acc, non_blocking=True)
             torch.cuda.current_stream().synchronize()
@@ -294,6 +331,37 @@ class LLM:
                 if self._emit(r, pin_out[i, :a + 1].tolist()):
                     self._finish_row(r, rows)
         self.stats = dict(steps=steps, accepted=accepted, decode_s=t_decode, bucket=B)
+
+    def _delta_step(self, st, B, graph, kp1):
+        """After a decode step: feed routing to the delta tier's frequency policy and,
+        with the confidence gate, promote this step's routed experts to FP4 and
+        replay the step while the verify rows are not confident."""
+        pairs = self._routed_pairs(B)
+        for li, e in pairs:
+            self.delta.note_routed(li, [e])
+        if self.gate is not None:
+            rows = torch.nonzero(st.active_rows).flatten()
+            logits = self.runner.main_logits(B)
+            step = (graph.replay if graph is not None else (lambda: self.runner.decode_body(st)))
+            snap = self._delta_snap
+
+            def run_step():
+                st.restore(snap)
+                step()
+                return logits[rows]
+            # the step already ran once: score it, fire, replay (at most gate_fp_max times)
+            score = self.gate.score(logits[rows])
+            fired = 0
+            while fired < self.gate.fp_max and self.gate.should_fire(score):
+                promote = [p for p in self._routed_pairs(B) if not self.delta.resident(*p)][: self.gate.max_promote]
+                if not promote or self.delta.promote(promote) == 0:
+                    break
+                score = self.gate.score(run_step())
+                fired += 1
+            self.delta.stats["gate_replays"] += fired
+        else:
+            self.delta.tick()
+        self.delta.step_end()
 
     def _finish_row(self, r, rows):
         rows[r.row] = None

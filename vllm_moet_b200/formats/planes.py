@@ -175,3 +175,60 @@ def quintal_plane_bytes(n: int, k: int) -> int:
 
 def dequant_plane(codes_plane: torch.Tensor, scale_plane: torch.Tensor, N: int, K: int) -> torch.Tensor:
     return dequant_codes(unpack_codes(codes_plane, N, K), unpack_scales(scale_plane, N, K))
+
+
+# ---------------------------------------------------------------------------
+# FP4 delta tier in an 8-bit container ("direct-8" plane).
+#
+# An MXFP4 weight (e2m1 value x UE8M0 block-32 scale) is exactly representable
+# as an e4m3 byte times the same scale, so the delta tier stores e4m3 bytes in
+# the order the 2-bit decode would produce A-fragments: per 16-row x 64-k
+# block and lane (g, t), 32 bytes = registers A0[0..3] (k32 = 0) then
+# A1[0..3] (k32 = 1), each register = tile (row g / g+8) x j-parity (j in
+# {0,2} or {1,3}), bytes [half0 j_a, half0 j_b, half1 j_a, half1 j_b].  The
+# expert GEMV then loads two 16-byte vectors per chunk and needs no decode;
+# activations keep the 2-bit path's "w2 layout".  2x the bytes of a nibble
+# plane, which HBM affords for the hot fraction of experts.
+
+def mxfp4_quantize(w: torch.Tensor):
+    """[N, K] float -> (e2m1 nibbles [N, K] u8, UE8M0 block-32 scales [N, K/32] u8)."""
+    from .codebook import e2m1_round
+    N, K = w.shape
+    x = w.double().reshape(N, K // 32, 32)
+    amax = x.abs().amax(-1)
+    # smallest power of two with amax / 2^e <= 6 (e2m1 max)
+    e = torch.ceil(torch.log2(torch.where(amax > 0, amax / 6.0, torch.ones_like(amax)))).clamp(-127, 127)
+    e = torch.where(amax > 0, e, torch.full_like(e, -127))
+    nib = e2m1_round((x / torch.exp2(e)[..., None]).float()).reshape(N, K)
+    return nib.to(torch.uint8), (e + 127).to(torch.uint8)
+
+
+def e2m1_to_e4m3_bytes(nib: torch.Tensor) -> torch.Tensor:
+    from .codebook import E2M1_VALUES
+    v = E2M1_VALUES.float().to(nib.device)[nib.long()]
+    return v.to(torch.float8_e4m3fn).view(torch.uint8)
+
+
+def pack_direct8(e4m3: torch.Tensor) -> torch.Tensor:
+    """[N, K] e4m3 bytes -> direct-8 plane [N*K] u8 (fragment register order)."""
+    v = _to_lane_order(e4m3)                      # [nb, kb, g, t, tile, k32, half, j]
+    v = v.reshape(*v.shape[:4], 2, 2, 2, 2, 2)    # j -> (j_hi, parity): j = 2*j_hi + parity
+    # target per lane: [k32][parity][tile][half][j_hi]
+    v = v.permute(0, 1, 2, 3, 5, 8, 4, 6, 7).contiguous()
+    return v.reshape(-1)
+
+
+def unpack_direct8(plane: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    v = plane.reshape(N // 16, K // 64, 8, 4, 2, 2, 2, 2, 2)     # k32, parity, tile, half, j_hi
+    v = v.permute(0, 1, 2, 3, 6, 4, 7, 8, 5).contiguous()        # tile, k32, half, j_hi, parity
+    return _from_lane_order(v.reshape(N // 16, K // 64, 8, 4, 2, 2, 2, 4), N, K)
+
+
+def direct8_plane_bytes(n: int, k: int) -> int:
+    return n * k
+
+
+def dequant_direct8(plane: torch.Tensor, scale_plane: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    b = unpack_direct8(plane, N, K).view(torch.float8_e4m3fn).float()
+    s = torch.exp2(unpack_scales(scale_plane, N, K).float() - 127.0)
+    return (b.view(N, K // 32, 32) * s[..., None]).view(N, K)

@@ -128,6 +128,7 @@ class ExpertPool:
     # CPU tiny config with fp16 group scales keeps dequantized matrices instead
     dense_w13: Optional[torch.Tensor] = None
     dense_w2: Optional[torch.Tensor] = None
+    delta_rows: Optional[torch.Tensor] = None     # [E, delta slot bytes] FP4 delta-tier rows (host)
 
     def dequant_expert(self, e: int):
         """-> (w13 [2I, H], w2 [H, I]) float32."""
@@ -291,7 +292,7 @@ def _shard_ffn(gu: torch.Tensor, down: torch.Tensor, I: int, tp_rank: int, tp_si
 
 
 def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0, tp_size=1,
-                expert_chunk: int = 16) -> LayerWeights:
+                expert_chunk: int = 16, with_delta: bool = False) -> LayerWeights:
     """One decoder layer, sharded for rank `tp_rank` of a `tp_size` tensor-parallel
     group.  Full matrices are drawn first (the same draws for every TP size) and
     then sliced, so TP runs compute the same function as one GPU:
@@ -370,6 +371,7 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
                                 dense_w13=torch.stack(w13s), dense_w2=torch.stack(w2s))
         return lw
     pool = torch.empty(E, layout.slot_bytes, dtype=torch.uint8, device=dev)
+    delta_rows = [] if with_delta else None
     for e0 in range(0, E, expert_chunk):
         n = min(expert_chunk, E - e0)
         w13 = shard13(rng.normal((n, 2 * Ifull, H)))
@@ -378,8 +380,13 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
             quantize_experts_gpu(w13, w2, layout, pool[e0:e0 + n])
         else:
             quantize_experts_cpu(w13, w2, layout, pool[e0:e0 + n])
+        if delta_rows is not None:       # FP4 delta-tier rows of the same experts (host side)
+            from ..residency.delta import pack_delta_slot
+            delta_rows += [pack_delta_slot(w13[i], w2[i]) for i in range(n)]
         del w13, w2
     lw.experts = ExpertPool(layout, pool, torch.arange(E, dtype=torch.int32, device=dev))
+    if delta_rows is not None:
+        lw.experts.delta_rows = torch.stack(delta_rows)
     return lw
 
 
@@ -402,7 +409,7 @@ def pp_layer_range(num_layers: int, pp_rank: int, pp_size: int):
 
 def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int = 0, tp_size: int = 1,
                    with_mtp: bool = True, num_layers: Optional[int] = None, pp_rank: int = 0,
-                   pp_size: int = 1) -> ModelWeights:
+                   pp_size: int = 1, with_delta: bool = False) -> ModelWeights:
     """Synthetic random-init weights of the given architecture (N(0, 0.02)).
     With pp_size > 1 only the stage's layers are built; the first stage holds
     the embedding, the last the final norm, the head and the MTP module."""
@@ -414,7 +421,8 @@ def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int =
     first, last = pp_rank == 0, pp_rank == pp_size - 1
     rng.counter = 0
     embed = rng.normal((cfg.vocab, H)).to(torch.bfloat16) if first else None
-    layers = [_make_layer(cfg, rng, i, dev, cfg.is_moe_layer(i), tp_rank, tp_size) for i in range(l0, l1)]
+    layers = [_make_layer(cfg, rng, i, dev, cfg.is_moe_layer(i), tp_rank, tp_size, with_delta=with_delta)
+              for i in range(l0, l1)]
     head = None
     if last:
         rng.counter = 1
@@ -434,6 +442,6 @@ def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int =
             enorm=torch.ones(H, dtype=torch.bfloat16, device=dev),
             hnorm=torch.ones(H, dtype=torch.bfloat16, device=dev),
             eh_proj=eh,
-            layer=_make_layer(cfg, rng, L, dev, True, tp_rank, tp_size),
+            layer=_make_layer(cfg, rng, L, dev, True, tp_rank, tp_size, with_delta=with_delta),
             head_norm=torch.ones(H, dtype=torch.bfloat16, device=dev))
     return mw

@@ -1,0 +1,89 @@
+"""FP4 delta tier: hot experts served at FP4 precision on the GPU.
+
+Each delta slot holds an expert's MXFP4 weights (e2m1 values, UE8M0 block-32
+scales) in the direct-8 container (:func:`formats.planes.pack_direct8`):
+``[w13 e4m3 (2I*H) | sc13 | w2 e4m3 (H*I) | sc2]``.  The expert GEMV checks
+the delta slot table first and reads the delta slot when present, else the
+2-bit base (reference: FP4 delta tier and its slot coupling, patch
+P:8063-8383, P:10290-10350).  Policies:
+
+* ``freq`` -- the manager promotes the most frequently routed experts
+  (recency-decayed counts) every ``tick``;
+* ``need`` -- only the confidence gate fills the pool (promote this step's
+  routed experts, then replay the step);
+* ``lru``  -- like ``need``, evicting the least recently used slot.
+
+The pool / table / host-store machinery is :class:`.tier.ExpertCache`.
+"""
+from __future__ import annotations
+
+from typing import List, Tuple
+
+import torch
+
+from ..formats import planes
+from .stores import make_store
+from .tier import ExpertCache
+
+
+def delta_layout(H: int, I: int):
+    """-> (slot_bytes, codes13, sc13, codes2, sc2 offsets) of a direct-8 delta slot."""
+    c13 = planes.direct8_plane_bytes(2 * I, H)
+    s13 = planes.scale_plane_bytes(2 * I, H)
+    c2 = planes.direct8_plane_bytes(H, I)
+    s2 = planes.scale_plane_bytes(H, I)
+    return c13 + s13 + c2 + s2, 0, c13, c13 + s13, c13 + s13 + c2
+
+
+def pack_delta_slot(w13: torch.Tensor, w2: torch.Tensor) -> torch.Tensor:
+    """float expert matrices w13 [2I, H], w2 [H, I] -> one delta slot row (u8)."""
+    parts = []
+    for m in (w13, w2):
+        nib, sc = planes.mxfp4_quantize(m)
+        parts.append(planes.pack_direct8(planes.e2m1_to_e4m3_bytes(nib)))
+        parts.append(planes.pack_scales(sc))
+    return torch.cat([p.cpu() for p in parts])
+
+
+def dequant_delta_slot(row: torch.Tensor, H: int, I: int):
+    sb, o13, os13, o2, os2 = delta_layout(H, I)
+    w13 = planes.dequant_direct8(row[o13:os13], row[os13:o2], 2 * I, H)
+    w2 = planes.dequant_direct8(row[o2:os2], row[os2:sb], H, I)
+    return w13, w2
+
+
+class DeltaTier(ExpertCache):
+    def __init__(self, rows_per_layer: List[torch.Tensor], H: int, I: int, n_slots: int, device="cuda",
+                 policy: str = "freq", decay: float = 0.98):
+        L = len(rows_per_layer)
+        E = rows_per_layer[0].shape[0]
+        self.layout = delta_layout(H, I)
+        sb = self.layout[0]
+        store = make_store("pinned", L, E, sb)
+        for li, r in enumerate(rows_per_layer):
+            store.add_layer(li, r)
+        super().__init__(store, L, E, sb, n_slots, device=device, policy="lru" if policy == "lru" else "freq",
+                         decay=decay, manager=True)
+        self.delta_policy = policy
+
+    @property
+    def offsets(self):
+        _, o13, _, o2, _ = self.layout
+        return o13, self.layout[2], o2, self.layout[4]
+
+    def tick(self, max_promote: int = 64) -> int:
+        """freq policy: promote the hottest non-resident experts (host-side, between steps)."""
+        if self.delta_policy != "freq":
+            return 0
+        with self.lock:
+            hot = torch.argsort(self.freq.view(-1), descending=True)[: self.n_slots]
+            want: List[Tuple[int, int]] = []
+            for i in hot.tolist():
+                li, e = divmod(int(i), self.E)
+                if float(self.freq[li, e]) <= 0:
+                    break
+                if int(self.mirror[li, e]) < 0:
+                    want.append((li, e))
+                if len(want) >= max_promote:
+                    break
+        return self.promote(want) if want else 0
