@@ -44,6 +44,7 @@ def main():
     ap.add_argument("--prefill-len", type=int, default=8192)
     ap.add_argument("--streams", type=int, default=32)
     ap.add_argument("--skip-extra", action="store_true", help="skip the 32-stream and prefill measurements")
+    ap.add_argument("--ep", action="store_true", help="N>1: experts partitioned across ranks instead of sharded")
     args = ap.parse_args()
     if args.impl == "reference":
         return _reference_arm(args)
@@ -68,7 +69,7 @@ def main():
     max_len = max(args.prompt_len + args.steps * 3 + args.warmup * 3 + 64, args.prefill_len + 64)
     llm = LLM("ds4-flash-shape", device="cuda", num_speculative_tokens=2, max_model_len=max_len,
               max_num_seqs=args.streams, num_layers=args.layers, seed=0, tensor_parallel_size=world,
-              tp_group=dist.group.WORLD if world > 1 else None, tp_rank=rank)
+              tp_group=dist.group.WORLD if world > 1 else None, tp_rank=rank, expert_parallel=args.ep and world > 1)
 
     def maxr(v):   # max over ranks of a time-like value
         if world == 1:
@@ -183,7 +184,8 @@ def main():
             "data": "synthetic prompts, random-init weights (N(0,0.02)) of the DS4-Flash shape",
             "config": {"model": "ds4-flash-shape (32 layers, hidden 4096, 256 experts top-8, MLA, MTP k=2)",
                        "global_batch": 1, "seq_len": args.prompt_len, "parallelism": (f"tp{world} (fused peer-memory all-reduce)" if llm.runner.ar is not None
-                                                else f"tp{world} (NCCL all-reduce)") if world > 1 else "single",
+                                                else f"tp{world} (NCCL all-reduce)") + (" + ep" if args.ep else "")
+                            if world > 1 else "single",
                        "l2": "inputs larger than L2 (each step streams ~7 GB of weights)",
                        "layers": args.layers or 32},
             "mtp_acceptance_per_step": round(acc, 4), "steps_per_s": round(1000.0 / ms, 2),

@@ -21,13 +21,13 @@ void router_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_
                  torch::Tensor wts);
 void build_pairs(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor rank_scratch,
                  torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
-                 torch::Tensor status);
+                 torch::Tensor status, int64_t e_lo);
 void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out);
 void moe_route_fused(torch::Tensor x, torch::Tensor w, torch::Tensor logits, c10::optional<torch::Tensor> bias,
                      int64_t k, bool sigmoid, int64_t n_group, int64_t topk_group, bool norm, double scaling,
                      torch::Tensor ids, torch::Tensor wts, int64_t MB, torch::Tensor rank_scratch,
                      torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
-                     torch::Tensor counter, torch::Tensor status);
+                     torch::Tensor counter, torch::Tensor status, int64_t e_lo, int64_t E_local);
 void mla_combine_uv(torch::Tensor o_part, torch::Tensor ml_part, torch::Tensor wuv, torch::Tensor swuv,
                     torch::Tensor q, torch::Tensor qs);
 void argmax_split(torch::Tensor logits, c10::optional<torch::Tensor> ids, c10::optional<torch::Tensor> lse,
@@ -36,7 +36,7 @@ void argmax_split(torch::Tensor logits, c10::optional<torch::Tensor> ids, c10::o
 void argmax_merge(torch::Tensor parts, torch::Tensor ids);
 void build_pairs_padded(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor rank_scratch,
                         torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
-                        torch::Tensor n_rows, torch::Tensor status);
+                        torch::Tensor n_rows, torch::Tensor status, int64_t e_lo);
 void gather_rows(torch::Tensor src_q, torch::Tensor src_s, torch::Tensor idx, torch::Tensor n_rows, torch::Tensor dst_q,
                  torch::Tensor dst_s);
 // moe_w2.cu
@@ -131,11 +131,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_fp8", &gemv_fp8, py::arg("a"), py::arg("sa"), py::arg("w"), py::arg("sw"), py::arg("out"),
         py::arg("resid"), py::arg("ar") = py::none());
   m.def("router_topk", &router_topk);
-  m.def("build_pairs", &build_pairs);
-  m.def("build_pairs_padded", &build_pairs_padded);
+  m.def("build_pairs", &build_pairs, py::arg("topk_ids"), py::arg("E"), py::arg("MB"), py::arg("rank_scratch"),
+        py::arg("sorted_tok"), py::arg("pos_of"), py::arg("pairs"), py::arg("n_pairs"), py::arg("status"),
+        py::arg("e_lo") = -1);
+  m.def("build_pairs_padded", &build_pairs_padded, py::arg("topk_ids"), py::arg("E"), py::arg("MB"),
+        py::arg("rank_scratch"), py::arg("sorted_tok"), py::arg("pos_of"), py::arg("pairs"), py::arg("n_pairs"),
+        py::arg("n_rows"), py::arg("status"), py::arg("e_lo") = -1);
   m.def("gather_rows", &gather_rows);
   m.def("router_logits", &router_logits);
-  m.def("moe_route_fused", &moe_route_fused);
+  m.def("moe_route_fused", &moe_route_fused, py::arg("x"), py::arg("w"), py::arg("logits"), py::arg("bias"),
+        py::arg("k"), py::arg("sigmoid"), py::arg("n_group"), py::arg("topk_group"), py::arg("norm"),
+        py::arg("scaling"), py::arg("ids"), py::arg("wts"), py::arg("MB"), py::arg("rank_scratch"),
+        py::arg("sorted_tok"), py::arg("pos_of"), py::arg("pairs"), py::arg("n_pairs"), py::arg("counter"),
+        py::arg("status"), py::arg("e_lo") = 0, py::arg("E_local") = 0);
   m.def("mla_combine_uv", &mla_combine_uv);
   m.def("tc_gemm_test", &tc_gemm_test);
   m.def("tc_moe_w2", &tc_moe_w2);

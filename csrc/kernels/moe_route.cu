@@ -213,15 +213,20 @@ __device__ __forceinline__ void build_pairs_block(const int* __restrict__ topk_i
                                                   int* __restrict__ rank_scratch, int* __restrict__ sorted_tok,
                                                   int* __restrict__ pos_of, int4* __restrict__ pairs,
                                                   int* __restrict__ n_pairs, int* __restrict__ status,
-                                                  int pad, int* __restrict__ n_rows) {
+                                                  int pad, int* __restrict__ n_rows, int e_lo = 0, int ep = 0) {
+  // ep != 0: expert parallelism -- this rank owns experts [e_lo, e_lo + E); routings to other
+  // experts are skipped (pos_of = -1, the combine ignores them); pairs carry local expert ids
   __shared__ int cnt[kMaxE];
   __shared__ int start[kMaxE];
   __shared__ int pstart[kMaxE];
   for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
   for (int r = threadIdx.x; r < R; r += blockDim.x) {
-    int e = topk_ids[r];
-    if (e < 0 || e >= E) { set_status(status, kBadIndex); e = 0; }
+    int e = topk_ids[r] - e_lo;
+    if (e < 0 || e >= E) {
+      if (ep) { rank_scratch[r] = -1; continue; }
+      set_status(status, kBadIndex); e = 0;
+    }
     rank_scratch[r] = atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
@@ -256,8 +261,11 @@ __device__ __forceinline__ void build_pairs_block(const int* __restrict__ topk_i
   }
   __syncthreads();
   for (int r = threadIdx.x; r < R; r += blockDim.x) {
-    int e = topk_ids[r];
-    if (e < 0 || e >= E) e = 0;
+    int e = topk_ids[r] - e_lo;
+    if (e < 0 || e >= E) {
+      if (ep) { pos_of[r] = -1; continue; }
+      e = 0;
+    }
     const int pos = start[e] + rank_scratch[r];
     sorted_tok[pos] = r / k;
     pos_of[r] = pos;
@@ -275,9 +283,10 @@ __global__ void build_pairs_kernel(const int* __restrict__ topk_ids, int R, int 
                                    int* __restrict__ rank_scratch, int* __restrict__ sorted_tok,
                                    int* __restrict__ pos_of, int4* __restrict__ pairs,
                                    int* __restrict__ n_pairs, int* __restrict__ status,
-                                   int pad = 0, int* __restrict__ n_rows = nullptr) {
+                                   int pad = 0, int* __restrict__ n_rows = nullptr, int e_lo = 0, int ep = 0) {
   pdl_entry();
-  build_pairs_block(topk_ids, R, k, E, MB, rank_scratch, sorted_tok, pos_of, pairs, n_pairs, status, pad, n_rows);
+  build_pairs_block(topk_ids, R, k, E, MB, rank_scratch, sorted_tok, pos_of, pairs, n_pairs, status, pad, n_rows,
+                    e_lo, ep);
 }
 
 // Decode routing in one launch: every CTA computes the router logits of 4
@@ -292,7 +301,8 @@ __global__ void __launch_bounds__(kRouteWarps * 32) moe_route_fused_kernel(
     float* __restrict__ logits, const float* __restrict__ bias, int k, int sigmoid, int n_group, int topk_group,
     int norm, float scaling, int* __restrict__ ids, float* __restrict__ wts, int MB,
     int* __restrict__ rank_scratch, int* __restrict__ sorted_tok, int* __restrict__ pos_of,
-    int4* __restrict__ pairs, int* __restrict__ n_pairs, int* __restrict__ counter, int* __restrict__ status) {
+    int4* __restrict__ pairs, int* __restrict__ n_pairs, int* __restrict__ counter, int* __restrict__ status,
+    int e_lo, int E_local, int ep) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int el = warp >> 2, qh = warp & 3;
   const int e = blockIdx.x * kRouteExperts + el;
@@ -361,7 +371,8 @@ __global__ void __launch_bounds__(kRouteWarps * 32) moe_route_fused_kernel(
     topk_token(logits, bias, t, E, k, sigmoid, n_group, topk_group, norm, scaling, ids, wts);
   __syncthreads();
   __threadfence_block();
-  build_pairs_block(ids, T * k, k, E, MB, rank_scratch, sorted_tok, pos_of, pairs, n_pairs, status, 0, nullptr);
+  build_pairs_block(ids, T * k, k, ep ? E_local : E, MB, rank_scratch, sorted_tok, pos_of, pairs, n_pairs, status,
+                    0, nullptr, e_lo, ep);
   if (threadIdx.x == 0) *counter = 0;
 }
 
@@ -421,8 +432,9 @@ void moe_route_fused(torch::Tensor x, torch::Tensor w, torch::Tensor logits, c10
                      int64_t k, bool sigmoid, int64_t n_group, int64_t topk_group, bool norm, double scaling,
                      torch::Tensor ids, torch::Tensor wts, int64_t MB, torch::Tensor rank_scratch,
                      torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
-                     torch::Tensor counter, torch::Tensor status) {
+                     torch::Tensor counter, torch::Tensor status, int64_t e_lo, int64_t E_local) {
   const int T = x.size(0), H = x.size(1), E = w.size(0);
+  const int ep = E_local > 0 ? 1 : 0;
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.is_contiguous() &&
               w.is_contiguous() && H % 1024 == 0, "moe_route_fused: bf16 contiguous, H % 1024 == 0");
   TORCH_CHECK(E <= kRouteWarps * 32 && k <= 32 && n_group <= 64, "moe_route_fused: E <= 512, k <= 32");
@@ -438,7 +450,7 @@ void moe_route_fused(torch::Tensor x, torch::Tensor w, torch::Tensor logits, c10
            (int)k, sigmoid ? 1 : 0, (int)n_group, (int)topk_group, norm ? 1 : 0, (float)scaling,
            ids.data_ptr<int>(), wts.data_ptr<float>(), (int)MB, rank_scratch.data_ptr<int>(),
            sorted_tok.data_ptr<int>(), pos_of.data_ptr<int>(), (int4*)pairs.data_ptr<int>(), n_pairs.data_ptr<int>(),
-           counter.data_ptr<int>(), status.data_ptr<int>());
+           counter.data_ptr<int>(), status.data_ptr<int>(), (int)e_lo, (int)E_local, ep);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -458,7 +470,7 @@ void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out) {
 // sorted_tok / pos_of must hold R / MB * MB + min(E, R) * MB rows.
 void build_pairs_padded(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor rank_scratch,
                         torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
-                        torch::Tensor n_rows, torch::Tensor status) {
+                        torch::Tensor n_rows, torch::Tensor status, int64_t e_lo) {
   const int T = topk_ids.size(0), k = topk_ids.size(1), R = T * k;
   TORCH_CHECK(E <= kMaxE, "build_pairs_padded: E <= 512");
   const int64_t P = R / MB + std::min<int64_t>(E, R);
@@ -467,13 +479,14 @@ void build_pairs_padded(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Te
   launch_k(build_pairs_kernel, 1, 1024, 0, stream, topk_ids.data_ptr<int>(), R, k, (int)E, (int)MB,
                                              rank_scratch.data_ptr<int>(), sorted_tok.data_ptr<int>(),
                                              pos_of.data_ptr<int>(), (int4*)pairs.data_ptr<int>(),
-                                             n_pairs.data_ptr<int>(), status.data_ptr<int>(), 1, n_rows.data_ptr<int>());
+                                             n_pairs.data_ptr<int>(), status.data_ptr<int>(), 1, n_rows.data_ptr<int>(),
+                                             (int)std::max<int64_t>(e_lo, 0), e_lo >= 0 ? 1 : 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 void build_pairs(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor rank_scratch,
                  torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
-                 torch::Tensor status) {
+                 torch::Tensor status, int64_t e_lo) {
   const int T = topk_ids.size(0), k = topk_ids.size(1), R = T * k;
   TORCH_CHECK(E <= kMaxE, "build_pairs: E <= 512");
   TORCH_CHECK(pairs.size(0) >= R / MB + std::min<int64_t>(E, R), "build_pairs: pairs buffer too small");
@@ -481,7 +494,8 @@ void build_pairs(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor ra
   launch_k(build_pairs_kernel, 1, 1024, 0, stream, topk_ids.data_ptr<int>(), R, k, (int)E, (int)MB,
                                              rank_scratch.data_ptr<int>(), sorted_tok.data_ptr<int>(),
                                              pos_of.data_ptr<int>(), (int4*)pairs.data_ptr<int>(),
-                                             n_pairs.data_ptr<int>(), status.data_ptr<int>(), 0, (int*)nullptr);
+                                             n_pairs.data_ptr<int>(), status.data_ptr<int>(), 0, (int*)nullptr,
+                                             (int)std::max<int64_t>(e_lo, 0), e_lo >= 0 ? 1 : 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -33,3 +33,26 @@ def test_tp2_forward_matches_single_rank():
         assert v_local * 2 == vocab
         assert err <= 1e-4 * max(scale, 1.0), (err, scale)
         assert mtp_err <= 1e-4 * max(scale, 1.0), mtp_err
+
+
+def _ep_forward(rank, world):
+    import torch.distributed as dist
+    cfg = tiny_config()
+    toks = torch.tensor([5, 17, 300, 42, 7, 99, 3, 250])
+    pos = torch.arange(len(toks))
+    cs = ref.rope_cos_sin(cfg, 64)
+    want, _ = ref.forward(random_weights(cfg, "cpu", seed=4), toks, pos, cs)
+    mw = random_weights(cfg, "cpu", seed=4, tp_rank=rank, tp_size=world, expert_parallel=True)
+    ex = mw.layers[0].experts
+    with ref.tp_context(dist.group.WORLD):
+        got, _ = ref.forward(mw, toks, pos, cs)
+    return float((got - want).abs().max()), float(want.abs().max()), ex.e_lo, ex.n_local
+
+
+def test_ep2_forward_matches_single_rank():
+    """Expert parallelism inside the TP group: each rank holds half of the experts
+    whole (attention still head-sharded); the summed partials equal one rank."""
+    res = run_ranks(_ep_forward, 2)
+    assert [(r[2], r[3]) for r in res] == [(0, 4), (4, 4)]
+    for err, scale, _, _ in res:
+        assert err <= 1e-4 * max(scale, 1.0), (err, scale)

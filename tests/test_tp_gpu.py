@@ -43,7 +43,7 @@ def _small_cfg():
                             dense_intermediate=512, num_heads=8, q_lora_rank=256, top_k=4)
 
 
-def _tp_engine(rank, world, fused):
+def _tp_engine(rank, world, fused, ep=False):
     import torch.distributed as dist
     from vllm_moet_b200 import SamplingParams
     from vllm_moet_b200.engine.llm import LLM
@@ -51,7 +51,7 @@ def _tp_engine(rank, world, fused):
     os.environ["MOET_TP_FUSED"] = "1" if fused else "0"     # read by set_tp_group
     cfg = _small_cfg()
     llm = LLM(cfg, device="cuda", num_speculative_tokens=2, max_model_len=512, max_num_seqs=2,
-              tensor_parallel_size=world, tp_group=dist.group.WORLD, tp_rank=rank)
+              tensor_parallel_size=world, tp_group=dist.group.WORLD, tp_rank=rank, expert_parallel=ep)
     g = torch.Generator().manual_seed(7)
     prompts = [torch.randint(3, 2048, (n,), generator=g).tolist() for n in (37, 64)]
     outs = [o.outputs[0].token_ids for o in llm.generate(prompts, SamplingParams(max_tokens=10, ignore_eos=True))]
@@ -100,3 +100,12 @@ def _pp_engine(rank, world):
 def test_pp2_matches_single_gpu():
     (o0, ref), (o1, _) = run_ranks(_pp_engine, 2, backend="nccl", env={"NCCL_NVLS_ENABLE": "0"})
     assert o0 == o1 == ref
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep2_engine_tracks_oracle():
+    """Expert parallelism inside the TP group (each rank owns half of the experts whole)."""
+    res = run_ranks(_tp_engine, 2, False, True, backend="nccl", env={"NCCL_NVLS_ENABLE": "0"})
+    (o0, w0), (o1, w1) = res
+    assert o0 == o1 and all(len(o) == 10 for o in o0)
+    assert max(w0, w1) < 0.5, (w0, w1)

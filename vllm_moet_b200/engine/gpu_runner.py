@@ -424,11 +424,15 @@ class NativeRunner:
         ex = lw.experts
         L = ex.layout
         I = L.I
+        # expert parallelism: this rank's experts are [e_lo, e_lo + E_loc); other routings are skipped
+        ep = ex.n_local is not None
+        E_loc = ex.n_local if ep else E
+        e_lo = ex.e_lo if ep else -1
         use_tc = ctx.mode == "prefill" and H % 128 == 0 and I % 128 == 0 and (2 * I) % 128 == 0
         if T <= 64 and not use_tc and H % 1024 == 0:
             # decode: logits + top-k + pair list in one launch
             MB = ctx.mb
-            P = R // MB + min(E, R)
+            P = R // MB + min(E_loc, R)
             rank = self.ws.get("rank", (R,), torch.int32)
             stok = self.ws.get("stok", (R,), torch.int32)
             posof = self.ws.get("posof", (R,), torch.int32)
@@ -437,7 +441,7 @@ class NativeRunner:
             cnt = self.ws.zeros("route.cnt", (1,), torch.int32)
             C.moe_route_fused(hb, self._router_w(lw), logits, lw.router_bias, k, cfg.router == "sigmoid",
                               cfg.n_group, cfg.topk_group, cfg.norm_topk_prob, cfg.routed_scaling, ids, wts, MB,
-                              rank, stok, posof, pairs, npairs, cnt, self.status)
+                              rank, stok, posof, pairs, npairs, cnt, self.status, max(e_lo, 0), E_loc if ep else 0)
             self._ensure_experts(mli, ids)
             y2 = self._moe_gemv_pairs(h2q, h2s, stok, pairs, npairs, ex, R, MB, mli)
         else:
@@ -449,9 +453,9 @@ class NativeRunner:
                           cfg.norm_topk_prob, cfg.routed_scaling, ids, wts)
             self._ensure_experts(mli, ids)
             if use_tc:
-                y2, posof = self._moe_tc(h2q, h2s, ids, ex, R, T)
+                y2, posof = self._moe_tc(h2q, h2s, ids, ex, R, T, E_loc, e_lo)
             else:
-                y2, posof = self._moe_gemv(h2q, h2s, ids, ex, R, ctx.mb, mli)
+                y2, posof = self._moe_gemv(h2q, h2s, ids, ex, R, ctx.mb, mli, E_loc, e_lo)
         if sh is not None:
             self._join()
         if self.tp_group is None:
@@ -465,11 +469,11 @@ class NativeRunner:
             self._tp_allreduce(part)
             torch.add(x, part, out=out)
 
-    def _moe_tc(self, h2q, h2s, ids, ex, R, T):
+    def _moe_tc(self, h2q, h2s, ids, ex, R, T, E=None, e_lo=-1):
         """Prefill experts on tensor cores: 128-row expert-aligned pairs, activations
         gathered into expert order, two warp-specialized tcgen05 GEMMs."""
         C, cfg = self.C, self.cfg
-        E, H = cfg.num_experts, cfg.hidden
+        E, H = E or cfg.num_experts, cfg.hidden
         L = ex.layout
         I = L.I
         MB = 128
@@ -481,7 +485,7 @@ class NativeRunner:
         pairs = self.ws.get("pairs", (P, 4), torch.int32)
         npairs = self.ws.get("npairs", (1,), torch.int32)
         nrows = self.ws.get("nrows", (1,), torch.int32)
-        C.build_pairs_padded(ids, E, MB, rank, stok, posof, pairs, npairs, nrows, self.status)
+        C.build_pairs_padded(ids, E, MB, rank, stok, posof, pairs, npairs, nrows, self.status, e_lo)
         xq = self.ws.get("xs.q", (Rp, H), torch.uint8)
         xs = self.ws.get("xs.s", (Rp, H // 64), torch.uint8)
         C.gather_rows(h2q, h2s, stok, nrows, xq, xs)
@@ -496,10 +500,10 @@ class NativeRunner:
                     self.miss, self.status, None)
         return y2, posof
 
-    def _moe_gemv(self, h2q, h2s, ids, ex, R, MB, mli=None):
+    def _moe_gemv(self, h2q, h2s, ids, ex, R, MB, mli=None, E=None, e_lo=-1):
         """Decode experts: mma.sync weight-streaming GEMV over the compact pair list."""
         C, cfg = self.C, self.cfg
-        E, H = cfg.num_experts, cfg.hidden
+        E, H = E or cfg.num_experts, cfg.hidden
         L = ex.layout
         I = L.I
         P = R // MB + min(E, R)
@@ -508,7 +512,7 @@ class NativeRunner:
         posof = self.ws.get("posof", (R,), torch.int32)
         pairs = self.ws.get("pairs", (P, 4), torch.int32)
         npairs = self.ws.get("npairs", (1,), torch.int32)
-        C.build_pairs(ids, E, MB, rank, stok, posof, pairs, npairs, self.status)
+        C.build_pairs(ids, E, MB, rank, stok, posof, pairs, npairs, self.status, e_lo)
         return self._moe_gemv_pairs(h2q, h2s, stok, pairs, npairs, ex, R, MB, mli), posof
 
     def _moe_gemv_pairs(self, h2q, h2s, stok, pairs, npairs, ex, R, MB, mli=None):

@@ -46,7 +46,7 @@ class LLM:
                  num_layers: Optional[int] = None, cuda_graphs: bool = True, num_gpu_blocks: Optional[int] = None,
                  tensor_parallel_size: int = 1, tp_group=None, tp_rank: int = 0,
                  pipeline_parallel_size: int = 1, pp_group=None, pp_rank: int = 0, expert_cache_slots: int = 0,
-                 delta_slots: int = 0, gate: Optional[bool] = None,
+                 delta_slots: int = 0, gate: Optional[bool] = None, expert_parallel: bool = False,
                  expert_store: str = "pinned", expert_store_dir: Optional[str] = None, **model_overrides):
         cfg = get_preset(model, **model_overrides) if isinstance(model, str) else model
         if num_layers is not None:
@@ -68,7 +68,7 @@ class LLM:
         self.mw = weights if weights is not None else random_weights(
             cfg, self.device, seed=seed, tp_rank=tp_rank, tp_size=tensor_parallel_size,
             with_mtp=num_speculative_tokens > 0, pp_rank=pp_rank, pp_size=pipeline_parallel_size,
-            with_delta=bool(delta_slots) and self.device.type == "cuda")
+            with_delta=bool(delta_slots) and self.device.type == "cuda", expert_parallel=expert_parallel)
         if pipeline_parallel_size > 1:
             # MTP presence is a property of the model, known on every stage
             self._has_mtp = num_speculative_tokens > 0 and cfg.num_mtp_layers > 0

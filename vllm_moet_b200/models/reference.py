@@ -129,9 +129,13 @@ def _stable_topk(x: torch.Tensor, k: int) -> torch.Tensor:
 def moe_block(cfg: ModelConfig, lw: LayerWeights, h: torch.Tensor) -> torch.Tensor:
     ids, w = route(cfg, lw, h)
     out = torch.zeros_like(h, dtype=torch.float32)
+    ex = lw.experts
+    lo, n_loc = ex.e_lo, ex.n_local
     for e in torch.unique(ids).tolist():
+        if n_loc is not None and not lo <= e < lo + n_loc:
+            continue            # expert parallelism: another rank owns this expert
         rows, slot = (ids == e).nonzero(as_tuple=True)
-        w13, w2 = lw.experts.dequant_expert(e)
+        w13, w2 = ex.dequant_expert(e - lo)
         y = swiglu(h[rows].float() @ w13.float().t(), cfg.swiglu_limit) @ w2.float().t()
         out.index_add_(0, rows, y * w[rows, slot, None])
     if lw.shared_gate_up is not None:

@@ -128,6 +128,8 @@ class ExpertPool:
     # CPU tiny config with fp16 group scales keeps dequantized matrices instead
     dense_w13: Optional[torch.Tensor] = None
     dense_w2: Optional[torch.Tensor] = None
+    e_lo: int = 0                  # expert parallelism: this rank holds experts [e_lo, e_lo + n_local)
+    n_local: Optional[int] = None
     delta_rows: Optional[torch.Tensor] = None     # [E, delta slot bytes] FP4 delta-tier rows (host)
 
     def dequant_expert(self, e: int):
@@ -292,7 +294,7 @@ def _shard_ffn(gu: torch.Tensor, down: torch.Tensor, I: int, tp_rank: int, tp_si
 
 
 def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0, tp_size=1,
-                expert_chunk: int = 16, with_delta: bool = False) -> LayerWeights:
+                expert_chunk: int = 16, with_delta: bool = False, ep: bool = False) -> LayerWeights:
     """One decoder layer, sharded for rank `tp_rank` of a `tp_size` tensor-parallel
     group.  Full matrices are drawn first (the same draws for every TP size) and
     then sliced, so TP runs compute the same function as one GPU:
@@ -341,8 +343,14 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
         lw.gate_up, lw.down = lin(gu.contiguous()), lin(dn.contiguous())
         return lw
     E, Ifull = cfg.num_experts, cfg.moe_intermediate
-    assert Ifull % tp_size == 0 and (Ifull // tp_size) % 64 == 0, "expert intermediate / tp must be a multiple of 64"
-    I = Ifull // tp_size
+    if ep:      # expert parallelism: whole experts, E / tp of them per rank
+        assert E % tp_size == 0, "num_experts must divide by the EP size"
+        I = Ifull
+        e_lo, n_loc = tp_rank * (E // tp_size), E // tp_size
+    else:       # tensor parallelism: every expert's intermediate dimension split
+        assert Ifull % tp_size == 0 and (Ifull // tp_size) % 64 == 0, "expert intermediate / tp must be a multiple of 64"
+        I = Ifull // tp_size
+        e_lo, n_loc = 0, E
     lw.router_w = rng.normal((E, H)).to(torch.bfloat16).float()   # bf16-valued gate weights
     lw.router_bias = torch.zeros(E, dtype=torch.float32, device=dev)
     if cfg.num_shared_experts:
@@ -351,7 +359,7 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
         gu, dn = _shard_ffn(rng.normal((2 * Is, H)), rng.normal((H, Is)), Is, tp_rank, tp_size, Isp)
         lw.shared_gate_up, lw.shared_down = lin(gu.contiguous()), lin(dn.contiguous())
     layout = ExpertLayout(H=H, I=I)
-    lo = tp_rank * I
+    lo = 0 if ep else tp_rank * I
 
     def shard13(w):   # [.., 2*Ifull, H] -> [.., 2I, H]
         return torch.cat([w[..., lo:lo + I, :], w[..., Ifull + lo:Ifull + lo + I, :]], dim=-2).contiguous()
@@ -369,13 +377,22 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
         pool = torch.zeros(E, 16, dtype=torch.uint8, device=dev)
         lw.experts = ExpertPool(layout, pool, torch.arange(E, dtype=torch.int32, device=dev),
                                 dense_w13=torch.stack(w13s), dense_w2=torch.stack(w2s))
+        if ep:
+            lw.experts.dense_w13 = lw.experts.dense_w13[e_lo:e_lo + n_loc]
+            lw.experts.dense_w2 = lw.experts.dense_w2[e_lo:e_lo + n_loc]
+            lw.experts.e_lo, lw.experts.n_local = e_lo, n_loc
         return lw
-    pool = torch.empty(E, layout.slot_bytes, dtype=torch.uint8, device=dev)
+    pool = torch.empty(n_loc, layout.slot_bytes, dtype=torch.uint8, device=dev)
     delta_rows = [] if with_delta else None
     for e0 in range(0, E, expert_chunk):
         n = min(expert_chunk, E - e0)
-        w13 = shard13(rng.normal((n, 2 * Ifull, H)))
-        w2 = shard2(rng.normal((n, H, Ifull)))
+        a, b = max(e0, e_lo), min(e0 + n, e_lo + n_loc)     # local experts of this chunk
+        if a >= b:
+            rng.counter += 2          # skip the chunk's two draws without generating them
+            continue
+        w13 = shard13(rng.normal((n, 2 * Ifull, H)))[a - e0:b - e0]
+        w2 = shard2(rng.normal((n, H, Ifull)))[a - e0:b - e0]
+        n, e0 = b - a, a - e_lo
         if torch.device(dev).type == "cuda":
             quantize_experts_gpu(w13, w2, layout, pool[e0:e0 + n])
         else:
@@ -384,7 +401,8 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
             from ..residency.delta import pack_delta_slot
             delta_rows += [pack_delta_slot(w13[i], w2[i]) for i in range(n)]
         del w13, w2
-    lw.experts = ExpertPool(layout, pool, torch.arange(E, dtype=torch.int32, device=dev))
+    lw.experts = ExpertPool(layout, pool, torch.arange(n_loc, dtype=torch.int32, device=dev), e_lo=e_lo,
+                            n_local=n_loc if ep else None)
     if delta_rows is not None:
         lw.experts.delta_rows = torch.stack(delta_rows)
     return lw
@@ -409,7 +427,7 @@ def pp_layer_range(num_layers: int, pp_rank: int, pp_size: int):
 
 def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int = 0, tp_size: int = 1,
                    with_mtp: bool = True, num_layers: Optional[int] = None, pp_rank: int = 0,
-                   pp_size: int = 1, with_delta: bool = False) -> ModelWeights:
+                   pp_size: int = 1, with_delta: bool = False, expert_parallel: bool = False) -> ModelWeights:
     """Synthetic random-init weights of the given architecture (N(0, 0.02)).
     With pp_size > 1 only the stage's layers are built; the first stage holds
     the embedding, the last the final norm, the head and the MTP module."""
@@ -421,8 +439,8 @@ def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int =
     first, last = pp_rank == 0, pp_rank == pp_size - 1
     rng.counter = 0
     embed = rng.normal((cfg.vocab, H)).to(torch.bfloat16) if first else None
-    layers = [_make_layer(cfg, rng, i, dev, cfg.is_moe_layer(i), tp_rank, tp_size, with_delta=with_delta)
-              for i in range(l0, l1)]
+    layers = [_make_layer(cfg, rng, i, dev, cfg.is_moe_layer(i), tp_rank, tp_size, with_delta=with_delta,
+                          ep=expert_parallel) for i in range(l0, l1)]
     head = None
     if last:
         rng.counter = 1
@@ -442,6 +460,6 @@ def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int =
             enorm=torch.ones(H, dtype=torch.bfloat16, device=dev),
             hnorm=torch.ones(H, dtype=torch.bfloat16, device=dev),
             eh_proj=eh,
-            layer=_make_layer(cfg, rng, L, dev, True, tp_rank, tp_size, with_delta=with_delta),
+            layer=_make_layer(cfg, rng, L, dev, True, tp_rank, tp_size, with_delta=with_delta, ep=expert_parallel),
             head_norm=torch.ones(H, dtype=torch.bfloat16, device=dev))
     return mw
