@@ -438,7 +438,8 @@ void moe_route_fused(torch::Tensor x, torch::Tensor w, torch::Tensor logits, c10
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.is_contiguous() &&
               w.is_contiguous() && H % 1024 == 0, "moe_route_fused: bf16 contiguous, H % 1024 == 0");
   TORCH_CHECK(E <= kRouteWarps * 32 && k <= 32 && n_group <= 64, "moe_route_fused: E <= 512, k <= 32");
-  TORCH_CHECK(pairs.size(0) >= (int64_t)T * k / MB + std::min<int64_t>(E, (int64_t)T * k), "moe_route_fused: pairs");
+  const int64_t Ep = E_local > 0 ? E_local : E;
+  TORCH_CHECK(pairs.size(0) >= (int64_t)T * k / MB + std::min<int64_t>(Ep, (int64_t)T * k), "moe_route_fused: pairs");
   if (T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   const size_t smem = (size_t)4 * H * 2;

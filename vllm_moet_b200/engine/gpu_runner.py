@@ -163,7 +163,7 @@ class NativeRunner:
                 return
         if T > 128 and K % 128 == 0 and lin.w.dim() == 2 and aq.stride(0) % 16 == 0:
             self.C.tc_gemm_fp8(aq, as_, lin.w, lin.s, out, resid, 128, self.status)
-        elif (T <= 8 and lin.w.dim() == 2 and K % 128 == 0 and K <= 6144 and aq.stride(0) % 16 == 0
+        elif (T <= 8 and lin.w.dim() == 2 and K % 128 == 0 and K <= 5120 and aq.stride(0) % 16 == 0
               and self.gemv_stream):
             # persistent TMA-ring GEMV: weight rows stream through shared memory continuously
             self.C.gemv_stream_fp8(aq, as_, lin.w, lin.s, out, resid, self.status)
@@ -320,7 +320,7 @@ class NativeRunner:
         # RMSNorm launches); needs no pending TP reduction and no indexer (which reads hq / qa)
         fuse = (ctx.mode == "decode" and T <= 8 and self.gemv_stream and self._pend is None
                 and lw.idx_wq is None and isinstance(lw.qkv_a.w, torch.Tensor) and lw.qkv_a.w.dim() == 2
-                and H % 128 == 0 and ql % 128 == 0 and H <= 6144 and ql <= 6144)
+                and H % 128 == 0 and ql % 128 == 0 and H <= 5120 and ql <= 5120)
         if fuse:
             C.gemv_stream_fp8(None, None, lw.qkv_a.w, lw.qkv_a.s, qkva, None, self.status, x, lw.attn_norm,
                               cfg.rms_eps)

@@ -19,6 +19,8 @@ def main(argv=None):
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--reps", type=int, default=1)
     ap.add_argument("--prompt-len", type=int, default=1024)
+    ap.add_argument("--mode", choices=["decode", "prefill"], default="decode",
+                    help="profile the captured decode step, or one prefill of --prompt-len tokens")
     a = ap.parse_args(argv)
     from ..engine.llm import LLM
     B = a.batch
@@ -35,6 +37,19 @@ def main(argv=None):
         prompts.append(torch.randint(3, llm.cfg.vocab, (a.prompt_len,), generator=g).tolist())
     st.block_table.copy_(bt)
     r.prefill(prompts, [bt[i].tolist() for i in range(B)], list(range(B)), st)
+    if a.mode == "prefill":
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record()
+        r.prefill(prompts, [bt[i].tolist() for i in range(B)], list(range(B)), st)
+        e.record()
+        torch.cuda.synchronize()
+        print("ms/prefill", s.elapsed_time(e))
+        torch.cuda.profiler.start()
+        r.prefill(prompts, [bt[i].tolist() for i in range(B)], list(range(B)), st)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        return
     st.set_active(torch.ones(B, dtype=torch.int32, device="cuda"))
     gr = r.capture(st)
     for _ in range(3):
