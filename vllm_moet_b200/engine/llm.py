@@ -65,10 +65,21 @@ class LLM:
                                  kv_cache_dtype=kv_cache_dtype, num_speculative_tokens=num_speculative_tokens,
                                  cuda_graphs=cuda_graphs, seed=seed, device=str(self.device))
         self.tokenizer = ByteTokenizer(cfg.vocab)
+        self.expert_source = None
+        if weights is None and self.ecfg.moet.planes_cache:
+            # boot the expert planes from the persistent quantisation cache (first boot fills it)
+            from ..residency import PlanesCache, checkpoint_id
+            from ..residency.sources import PlanesSource
+            self.expert_source = PlanesSource(PlanesCache(
+                self.ecfg.moet.planes_cache, self.ecfg.moet.ckpt_id or checkpoint_id(cfg=cfg, seed=seed),
+                tp_world=tensor_parallel_size, tp_rank=tp_rank))
         self.mw = weights if weights is not None else random_weights(
             cfg, self.device, seed=seed, tp_rank=tp_rank, tp_size=tensor_parallel_size,
             with_mtp=num_speculative_tokens > 0, pp_rank=pp_rank, pp_size=pipeline_parallel_size,
-            with_delta=bool(delta_slots) and self.device.type == "cuda", expert_parallel=expert_parallel)
+            with_delta=bool(delta_slots) and self.device.type == "cuda", expert_parallel=expert_parallel,
+            expert_source=self.expert_source)
+        if self.expert_source is not None:
+            self.expert_source.flush()
         if pipeline_parallel_size > 1:
             # MTP presence is a property of the model, known on every stage
             self._has_mtp = num_speculative_tokens > 0 and cfg.num_mtp_layers > 0

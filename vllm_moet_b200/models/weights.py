@@ -294,7 +294,8 @@ def _shard_ffn(gu: torch.Tensor, down: torch.Tensor, I: int, tp_rank: int, tp_si
 
 
 def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0, tp_size=1,
-                expert_chunk: int = 16, with_delta: bool = False, ep: bool = False) -> LayerWeights:
+                expert_chunk: int = 16, with_delta: bool = False, ep: bool = False,
+                expert_source=None) -> LayerWeights:
     """One decoder layer, sharded for rank `tp_rank` of a `tp_size` tensor-parallel
     group.  Full matrices are drawn first (the same draws for every TP size) and
     then sliced, so TP runs compute the same function as one GPU:
@@ -384,6 +385,14 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
         return lw
     pool = torch.empty(n_loc, layout.slot_bytes, dtype=torch.uint8, device=dev)
     delta_rows = [] if with_delta else None
+    # boot from a persistent cache (planes cache / pack): the quantised rows of this layer
+    cached = expert_source.load(li, n_loc, layout.slot_bytes) if expert_source is not None and not with_delta else None
+    if cached is not None:
+        pool.copy_(cached.view(n_loc, layout.slot_bytes))
+        rng.counter += 2 * ((E + expert_chunk - 1) // expert_chunk)   # keep later draws aligned
+        lw.experts = ExpertPool(layout, pool, torch.arange(n_loc, dtype=torch.int32, device=dev), e_lo=e_lo,
+                                n_local=n_loc if ep else None)
+        return lw
     for e0 in range(0, E, expert_chunk):
         n = min(expert_chunk, E - e0)
         a, b = max(e0, e_lo), min(e0 + n, e_lo + n_loc)     # local experts of this chunk
@@ -403,6 +412,8 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
         del w13, w2
     lw.experts = ExpertPool(layout, pool, torch.arange(n_loc, dtype=torch.int32, device=dev), e_lo=e_lo,
                             n_local=n_loc if ep else None)
+    if expert_source is not None:        # streaming first-boot build: persist the layer as soon as it exists
+        expert_source.store(li, pool)
     if delta_rows is not None:
         lw.experts.delta_rows = torch.stack(delta_rows)
     return lw
@@ -427,7 +438,8 @@ def pp_layer_range(num_layers: int, pp_rank: int, pp_size: int):
 
 def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int = 0, tp_size: int = 1,
                    with_mtp: bool = True, num_layers: Optional[int] = None, pp_rank: int = 0,
-                   pp_size: int = 1, with_delta: bool = False, expert_parallel: bool = False) -> ModelWeights:
+                   pp_size: int = 1, with_delta: bool = False, expert_parallel: bool = False,
+                   expert_source=None) -> ModelWeights:
     """Synthetic random-init weights of the given architecture (N(0, 0.02)).
     With pp_size > 1 only the stage's layers are built; the first stage holds
     the embedding, the last the final norm, the head and the MTP module."""
@@ -440,7 +452,7 @@ def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int =
     rng.counter = 0
     embed = rng.normal((cfg.vocab, H)).to(torch.bfloat16) if first else None
     layers = [_make_layer(cfg, rng, i, dev, cfg.is_moe_layer(i), tp_rank, tp_size, with_delta=with_delta,
-                          ep=expert_parallel) for i in range(l0, l1)]
+                          ep=expert_parallel, expert_source=expert_source) for i in range(l0, l1)]
     head = None
     if last:
         rng.counter = 1
@@ -460,6 +472,7 @@ def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int =
             enorm=torch.ones(H, dtype=torch.bfloat16, device=dev),
             hnorm=torch.ones(H, dtype=torch.bfloat16, device=dev),
             eh_proj=eh,
-            layer=_make_layer(cfg, rng, L, dev, True, tp_rank, tp_size, with_delta=with_delta, ep=expert_parallel),
+            layer=_make_layer(cfg, rng, L, dev, True, tp_rank, tp_size, with_delta=with_delta, ep=expert_parallel,
+                              expert_source=expert_source),
             head_norm=torch.ones(H, dtype=torch.bfloat16, device=dev))
     return mw
