@@ -1,0 +1,106 @@
+"""Context parallelism for long sequences: decode context parallel (DCP)
+and sequence-parallel prefill (SP), as collective algorithms over a
+torch.distributed group.
+
+* :func:`lse_merge` -- merge per-shard attention outputs with their
+  log-sum-exps (exact; rank order fixed, so every rank gets identical bits).
+* :func:`dcp_decode_attention` -- each rank attends over its shard of the KV
+  (positions ``r, r + W, ...`` interleaved, or a contiguous range), then the
+  (o, lse) pairs are all-gathered and merged (reference: DCP combine with
+  LSE, patch P:2990-3027, ``cp_lse_ag_out_rs``).
+* :func:`dcp_topk` -- sparse-indexer top-k over a sharded key set: local
+  top-k, ids lifted to global positions, (score, id) all-gathered, global
+  top-k re-selected identically on all ranks (ties: lower id) (reference:
+  DCP sparse top-k, C39).
+* :func:`sp_prefill_attention` -- sequence-parallel prefill: every rank holds
+  a contiguous chunk of the prompt, all-gathers the chunks' (compressed) K/V
+  and runs causal attention for its own queries at its global offset
+  (new in this framework; the reference has no SP prefill).
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+def _world(group):
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def _all_gather(t: torch.Tensor, group) -> torch.Tensor:
+    W, _ = _world(group)
+    out = [torch.empty_like(t) for _ in range(W)]
+    dist.all_gather(out, t.contiguous(), group=group)
+    return torch.stack(out)
+
+
+def lse_merge(outs: torch.Tensor, lses: torch.Tensor) -> torch.Tensor:
+    """outs [W, ..., D], lses [W, ...] (natural log; -inf = empty shard) -> [..., D]."""
+    m = lses.max(dim=0).values
+    m = torch.where(torch.isinf(m), torch.zeros_like(m), m)
+    w = torch.exp(lses - m)                       # [W, ...]
+    den = w.sum(dim=0)
+    num = (w[..., None] * outs).sum(dim=0)
+    return num / den.clamp_min(1e-30)[..., None]
+
+
+def partial_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+                      mask: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """q [T, H, D], k [S, D] (shared by heads, MLA latent form), v [S, Dv] -> (o [T, H, Dv], lse [T, H])."""
+    s = torch.einsum("thd,sd->ths", q.float(), k.float()) * scale
+    if mask is not None:
+        s = s.masked_fill(~mask[:, None, :], float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    p = torch.exp(s - torch.where(torch.isinf(lse), torch.zeros_like(lse), lse)[..., None])
+    o = torch.einsum("ths,sd->thd", p, v.float())
+    return o, lse
+
+
+def dcp_decode_attention(q, k_local, v_local, scale, group, mask_local=None):
+    """q [T, H, D] replicated; k_local/v_local this rank's KV shard -> full attention [T, H, Dv]."""
+    o, lse = partial_attention(q, k_local, v_local, scale, mask_local)
+    return lse_merge(_all_gather(o, group), _all_gather(lse, group))
+
+
+def dcp_topk(scores_local: torch.Tensor, k: int, global_ids: torch.Tensor, group) -> torch.Tensor:
+    """scores_local [T, S_r] (-inf = invalid), global_ids [S_r] (position of each local key)
+    -> global top-k positions [T, k] (-1 padded), identical on every rank, ties to the lower id."""
+    T, S = scores_local.shape
+    kk = min(k, S)
+    # stable local selection: sort by (-score, id)
+    order = torch.argsort(global_ids)
+    sc, gid = scores_local[:, order], global_ids[order]
+    vals, idx = torch.sort(-sc, dim=1, stable=True)
+    vals, idx = -vals[:, :kk], idx[:, :kk]
+    ids = gid[idx]
+    ids = torch.where(torch.isinf(vals) & (vals < 0), torch.full_like(ids, -1), ids)
+    if kk < k:
+        vals = torch.cat([vals, torch.full((T, k - kk), float("-inf"), dtype=vals.dtype)], 1)
+        ids = torch.cat([ids, torch.full((T, k - kk), -1, dtype=ids.dtype)], 1)
+    av, ai = _all_gather(vals, group), _all_gather(ids, group)          # [W, T, k]
+    av = av.permute(1, 0, 2).reshape(T, -1)
+    ai = ai.permute(1, 0, 2).reshape(T, -1)
+    # global order: score desc, then id asc (ids are unique across ranks; -1 entries have -inf)
+    big = torch.iinfo(torch.int64).max
+    key_id = torch.where(ai < 0, torch.full_like(ai, big), ai)
+    o1 = torch.argsort(key_id, dim=1, stable=True)
+    av, ai = av.gather(1, o1), ai.gather(1, o1)
+    o2 = torch.argsort(-av, dim=1, stable=True)
+    out = ai.gather(1, o2)[:, :k]
+    return torch.where(torch.isinf(av.gather(1, o2)[:, :k]), torch.full_like(out, -1), out)
+
+
+def sp_prefill_attention(q_local, k_local, v_local, scale, group):
+    """Contiguous chunk per rank (equal lengths): q/k/v_local [Tc, ...] -> causal attention
+    of the local queries over all keys up to their global position."""
+    W, r = _world(group)
+    Tc = q_local.shape[0]
+    k_all = _all_gather(k_local, group).reshape(W * Tc, *k_local.shape[1:])
+    v_all = _all_gather(v_local, group).reshape(W * Tc, *v_local.shape[1:])
+    qpos = r * Tc + torch.arange(Tc)
+    mask = torch.arange(W * Tc)[None, :] <= qpos[:, None]
+    o, _ = partial_attention(q_local, k_all, v_all, scale, mask)
+    return o
