@@ -51,7 +51,8 @@ void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::
 // gemv_stream.cu
 void gemv_stream_fp8(c10::optional<torch::Tensor> a, c10::optional<torch::Tensor> sa, torch::Tensor w,
                      torch::Tensor sw, torch::Tensor out, c10::optional<torch::Tensor> resid, torch::Tensor status,
-                     c10::optional<torch::Tensor> x_norm, c10::optional<torch::Tensor> gamma, double eps);
+                     c10::optional<torch::Tensor> x_norm, c10::optional<torch::Tensor> gamma, double eps,
+                     c10::optional<torch::Tensor> x_add, c10::optional<torch::Tensor> x_out);
 // indexer.cu
 void indexer_logits(torch::Tensor q, torch::Tensor w, torch::Tensor k_cache, torch::Tensor block_table,
                     torch::Tensor seq_of_tok, torch::Tensor pos_of_tok, torch::Tensor out, torch::Tensor status);
@@ -165,7 +166,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("indexer_topk", &indexer_topk);
   m.def("gemv_stream_fp8", &gemv_stream_fp8, py::arg("a"), py::arg("sa"), py::arg("w"), py::arg("sw"), py::arg("out"),
         py::arg("resid"), py::arg("status"), py::arg("x_norm") = py::none(), py::arg("gamma") = py::none(),
-        py::arg("eps") = 1e-6);
+        py::arg("eps") = 1e-6, py::arg("x_add") = py::none(), py::arg("x_out") = py::none());
   m.def("idx_k_write", &idx_k_write);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);

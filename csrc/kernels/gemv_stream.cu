@@ -57,7 +57,28 @@ struct GemvStreamArgs {
   int* status;
   // optional fused RMSNorm + e4m3 quantisation of a bf16 input (replaces A / sA)
   const __nv_bfloat16* xin; long long xin_stride; const __nv_bfloat16* gamma; float eps;
+  // optional residual add before the norm: x = bf16(xin + xadd), written to xout by CTA 0
+  const __nv_bfloat16* xadd; __nv_bfloat16* xout; long long xadd_stride;
 };
+
+// 8 bf16 of row r at column c of (xin [+ xadd]), the sum rounded to bf16 as the residual stream stores it
+MOET_DEVICE void gs_load8(const GemvStreamArgs& p, int r, int c, float (&v)[8]) {
+  const uint4 a = *reinterpret_cast<const uint4*>(p.xin + (size_t)r * p.xin_stride + c);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&a);
+  if (p.xadd) {
+    const uint4 b = *reinterpret_cast<const uint4*>(p.xadd + (size_t)r * p.xadd_stride + c);
+    const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const float2 f = __bfloat1622float2(h[q]), g = __bfloat1622float2(hb[q]);
+      v[2 * q] = __bfloat162float(__float2bfloat16(f.x + g.x));
+      v[2 * q + 1] = __bfloat162float(__float2bfloat16(f.y + g.y));
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; q++) { const float2 f = __bfloat1622float2(h[q]); v[2 * q] = f.x; v[2 * q + 1] = f.y; }
+  }
+}
 
 __global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStreamArgs p) {
   using namespace gs;
@@ -109,14 +130,13 @@ __global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStr
     float* ssq = red;                                       // [T][ng] partial sums of squares
     for (int i = threadIdx.x; i < p.T * ng; i += blockDim.x) {
       const int r = i / ng, c = i % ng;
-      const uint4* xr = reinterpret_cast<const uint4*>(p.xin + (size_t)r * p.xin_stride + c * 64);
       float acc = 0.f;
 #pragma unroll
       for (int u = 0; u < 8; u++) {
-        const uint4 v = xr[u];
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+        float v[8];
+        gs_load8(p, r, c * 64 + u * 8, v);
 #pragma unroll
-        for (int q = 0; q < 4; q++) { const float2 f = __bfloat1622float2(h[q]); acc = fmaf(f.x, f.x, fmaf(f.y, f.y, acc)); }
+        for (int q = 0; q < 8; q++) acc = fmaf(v[q], v[q], acc);
       }
       ssq[i] = acc;
     }
@@ -132,20 +152,29 @@ __global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStr
       float tot = 0.f;
       for (int q = 0; q < ng; q++) tot += ssq[r * ng + q];
       const float rinv = rsqrtf(tot / (float)p.K + p.eps);
-      const uint4* xr = reinterpret_cast<const uint4*>(p.xin + (size_t)r * p.xin_stride + c * 64);
       const uint4* gr = reinterpret_cast<const uint4*>(p.gamma + c * 64);
       float y[64];
       float amax = 0.f;
 #pragma unroll
       for (int u = 0; u < 8; u++) {
-        const uint4 v = xr[u], gv = gr[u];
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+        float v[8];
+        gs_load8(p, r, c * 64 + u * 8, v);
+        if (p.xout && blockIdx.x == 0) {    // the summed residual stream, written once
+          uint32_t o[4];
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * q], v[2 * q + 1]);
+            o[q] = *reinterpret_cast<const uint32_t*>(&b2);
+          }
+          *reinterpret_cast<uint4*>(p.xout + (size_t)r * p.K + c * 64 + u * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        const uint4 gv = gr[u];
         const __nv_bfloat162* gg = reinterpret_cast<const __nv_bfloat162*>(&gv);
 #pragma unroll
         for (int q = 0; q < 4; q++) {
-          const float2 f = __bfloat1622float2(h[q]), g2 = __bfloat1622float2(gg[q]);
-          const float a = __bfloat162float(__float2bfloat16(f.x * rinv * g2.x));
-          const float b = __bfloat162float(__float2bfloat16(f.y * rinv * g2.y));
+          const float2 g2 = __bfloat1622float2(gg[q]);
+          const float a = __bfloat162float(__float2bfloat16(v[2 * q] * rinv * g2.x));
+          const float b = __bfloat162float(__float2bfloat16(v[2 * q + 1] * rinv * g2.y));
           y[u * 8 + 2 * q] = a; y[u * 8 + 2 * q + 1] = b;
           amax = fmaxf(amax, fmaxf(fabsf(a), fabsf(b)));
         }
@@ -227,7 +256,8 @@ using namespace moet;
 // Same contract as gemv_fp8 for unbatched weights, T <= 8, K % 64 == 0, K <= 8192.
 void gemv_stream_fp8(c10::optional<torch::Tensor> a_opt, c10::optional<torch::Tensor> sa_opt, torch::Tensor w,
                      torch::Tensor sw, torch::Tensor out, c10::optional<torch::Tensor> resid, torch::Tensor status,
-                     c10::optional<torch::Tensor> x_norm, c10::optional<torch::Tensor> gamma, double eps) {
+                     c10::optional<torch::Tensor> x_norm, c10::optional<torch::Tensor> gamma, double eps,
+                     c10::optional<torch::Tensor> x_add, c10::optional<torch::Tensor> x_out) {
   const bool fuse = x_norm.has_value() && x_norm->defined();
   const torch::Tensor& a = fuse ? *x_norm : *a_opt;
   const int T = a.size(0), K = w.size(1), N = w.size(0);
@@ -251,6 +281,13 @@ void gemv_stream_fp8(c10::optional<torch::Tensor> a_opt, c10::optional<torch::Te
   p.sA = fuse ? nullptr : (const uint8_t*)sa_opt->data_ptr(); p.sa_stride = fuse ? 0 : sa_opt->stride(0);
   p.xin = fuse ? (const __nv_bfloat16*)a.data_ptr() : nullptr; p.xin_stride = fuse ? a.stride(0) : 0;
   p.gamma = fuse ? (const __nv_bfloat16*)gamma->data_ptr() : nullptr; p.eps = (float)eps;
+  p.xadd = nullptr; p.xout = nullptr; p.xadd_stride = 0;
+  if (fuse && x_add.has_value() && x_add->defined()) {
+    TORCH_CHECK(x_add->scalar_type() == at::kBFloat16 && x_add->stride(1) == 1 && x_add->size(1) == K &&
+                x_out.has_value() && x_out->is_contiguous() && x_out->size(1) == K, "gemv_stream_fp8: x_add / x_out");
+    p.xadd = (const __nv_bfloat16*)x_add->data_ptr(); p.xadd_stride = x_add->stride(0);
+    p.xout = (__nv_bfloat16*)x_out->data_ptr();
+  }
   p.W = (const uint8_t*)w.data_ptr(); p.sW = (const uint8_t*)sw.data_ptr(); p.sw_cols = sw.size(1);
   p.out = out.data_ptr(); p.out_stride = out.stride(0); p.out_f32 = out.scalar_type() == at::kFloat;
   p.resid = resid.has_value() && resid->defined() ? (const __nv_bfloat16*)resid->data_ptr() : nullptr;

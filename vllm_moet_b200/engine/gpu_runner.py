@@ -115,6 +115,8 @@ class NativeRunner:
         self.delta = None         # residency.DeltaTier (FP4 hot experts) when enabled
         self._moe_index = {}
         self._pend = None         # (residual, out) of a pushed reduction the next RMSNorm completes
+        self._pend_add = None     # (residual, reduced partial, out): decode residual add left to the next norm
+        self._decode = False
         self._fused = False
         # pipeline parallelism: this stage's layers; first stage embeds, last stage owns head + MTP
         self.pp_group = None
@@ -255,7 +257,11 @@ class NativeRunner:
             torch.distributed.broadcast(t, src=src, group=self.pp_group)
 
     def _materialize(self, x):
-        """Complete a pending fused all-reduce into x (no norm outputs)."""
+        """Complete a pending fused all-reduce / residual add into x (no norm outputs)."""
+        if self._pend_add is not None:
+            x0, part, xout = self._pend_add
+            self._pend_add = None
+            torch.add(x0, part, out=xout)
         if self._pend is not None:
             resid, xout = self._pend
             self._pend = None
@@ -273,7 +279,11 @@ class NativeRunner:
         """RMSNorm + quant of a sublayer input; completes a pending fused
         all-reduce first (x = residual + sum of the ranks' partials, written to x)."""
         pend, self._pend = self._pend, None
-        if pend is not None:
+        padd, self._pend_add = self._pend_add, None
+        if padd is not None:      # x = residual + all-reduced partial, then the norm (one kernel)
+            x0, part, xout = padd
+            self.C.rmsnorm_quant(x0, part, xout, w, self.cfg.rms_eps, y_out, q0, s0, q1, s1, ostride)
+        elif pend is not None:
             resid, xout = pend
             assert xout.data_ptr() == x.data_ptr()
             self.C.rmsnorm_quant(resid, None, xout, w, self.cfg.rms_eps, y_out, q0, s0, q1, s1, ostride, self.ar.desc)
@@ -291,7 +301,10 @@ class NativeRunner:
             part = self.ws.get("rp_part", (T, self.cfg.hidden), torch.bfloat16)
             self._gemv(aq, as_, lin, part)
             self._tp_allreduce(part)
-            torch.add(x, part, out=out)
+            if self._decode:
+                self._pend_add = (x, part, out)     # the next norm adds the residual
+            else:
+                torch.add(x, part, out=out)
 
     def _fork(self):
         """Start a side branch: work issued under the returned context runs
@@ -322,8 +335,14 @@ class NativeRunner:
                 and lw.idx_wq is None and isinstance(lw.qkv_a.w, torch.Tensor) and lw.qkv_a.w.dim() == 2
                 and H % 128 == 0 and ql % 128 == 0 and H <= 5120 and ql <= 5120)
         if fuse:
-            C.gemv_stream_fp8(None, None, lw.qkv_a.w, lw.qkv_a.s, qkva, None, self.status, x, lw.attn_norm,
-                              cfg.rms_eps)
+            padd, self._pend_add = self._pend_add, None
+            if padd is not None:     # residual add of a pending TP reduction folded into the prologue
+                x0, part, xout = padd
+                C.gemv_stream_fp8(None, None, lw.qkv_a.w, lw.qkv_a.s, qkva, None, self.status, x0, lw.attn_norm,
+                                  cfg.rms_eps, part, xout)
+            else:
+                C.gemv_stream_fp8(None, None, lw.qkv_a.w, lw.qkv_a.s, qkva, None, self.status, x, lw.attn_norm,
+                                  cfg.rms_eps)
         else:
             self._norm_in(x, lw.attn_norm, None, hq, hs)
             self._gemv(hq, hs, lw.qkv_a, qkva)
@@ -467,7 +486,10 @@ class NativeRunner:
             part = self.ws.get("moe_part", (T, H), torch.bfloat16)
             C.moe_combine(y2, posof, wts, None, sh, part, None)
             self._tp_allreduce(part)
-            torch.add(x, part, out=out)
+            if self._decode:
+                self._pend_add = (x, part, out)
+            else:
+                torch.add(x, part, out=out)
 
     def _moe_tc(self, h2q, h2s, ids, ex, R, T, E=None, e_lo=-1):
         """Prefill experts on tensor cores: 128-row expert-aligned pairs, activations
@@ -538,7 +560,7 @@ class NativeRunner:
 
     def _check(self, name, t):
         """Debug aid (MOET_DEBUG_FINITE=1, eager only): raise at the first non-finite stage output."""
-        if self.debug_finite and self._pend is None and not torch.cuda.is_current_stream_capturing():
+        if self.debug_finite and self._pend is None and self._pend_add is None and not torch.cuda.is_current_stream_capturing():
             bad = ~torch.isfinite(t.float())
             if bool(bad.any()):
                 rows = bad.view(t.shape[0], -1).any(-1).nonzero().flatten()[:8].tolist()
@@ -547,6 +569,7 @@ class NativeRunner:
     def _layer(self, lw, x, ctx, cache, li):
         H = self.cfg.hidden
         self._fused = self.ar is not None and ctx.mode == "decode" and self.ar.fits(ctx.T, H)
+        self._decode = ctx.mode == "decode"
         x2 = self.ws.get("x_mid", (ctx.T, H), torch.bfloat16)
         self._attention(lw, x, ctx, cache, li, x2)
         self._check(f"attention[{li}] ({ctx.mode})", x2)
