@@ -256,3 +256,7 @@ def test_prefetchers(tmp_path):
     da = DraftAffinity(c)
     da.record([42], [torch.tensor([[5]]), None, torch.tensor([[6]])])
     assert da.prefetch([42]) == 2 and c.resident(0, 5) and c.resident(2, 6)
+
+
+def test_floor_caps_at_expert_count():
+    assert working_set_floor(3, 4, 2, 2, num_experts=16) == int(1.15 * 3 * 16 + 0.999)

@@ -31,8 +31,10 @@ def resident_tokens():
 
 
 @pytest.mark.parametrize("kind", ["pinned", "tiered"])
-def test_cached_experts_match_resident(resident_tokens, kind, tmp_path):
-    # 3 MoE layers (2 main + MTP) x 16 experts = 48; a 40-slot cache forces evictions and replays
+def test_cached_experts_match_resident(resident_tokens, kind, tmp_path, monkeypatch):
+    # 3 MoE layers (2 main + MTP) x 16 experts = 48; a 40-slot cache (below the conservative
+    # working-set floor, hence FORCE_POOL) forces evictions and replays
+    monkeypatch.setenv("VLLM_MOE_W2_FORCE_POOL", "1")
     llm = LLM(_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=512, max_num_seqs=2,
               expert_cache_slots=40, expert_store=kind, expert_store_dir=str(tmp_path))
     out = [o.outputs[0].token_ids for o in llm.generate(_prompts(), SamplingParams(max_tokens=12, ignore_eos=True))]
@@ -40,7 +42,7 @@ def test_cached_experts_match_resident(resident_tokens, kind, tmp_path):
     st = llm.cache.stats
     assert st["fetched_rows"] > 0
     assert llm.replay.stats["steps"] > 0
-    llm.cache.close()
+    llm.shutdown()
 
 
 def test_delta_tier_and_gate(resident_tokens):

@@ -448,7 +448,8 @@ class NativeRunner:
         E_loc = ex.n_local if ep else E
         e_lo = ex.e_lo if ep else -1
         use_tc = ctx.mode == "prefill" and H % 128 == 0 and I % 128 == 0 and (2 * I) % 128 == 0
-        if T <= 64 and not use_tc and H % 1024 == 0:
+        topp = self.ecfg.moet.topp
+        if T <= 64 and not use_tc and H % 1024 == 0 and topp <= 0:
             # decode: logits + top-k + pair list in one launch
             MB = ctx.mb
             P = R // MB + min(E_loc, R)
@@ -470,6 +471,11 @@ class NativeRunner:
                 torch.mm(hb.float(), lw.router_w.t(), out=logits)
             C.router_topk(logits, lw.router_bias, k, cfg.router == "sigmoid", cfg.n_group, cfg.topk_group,
                           cfg.norm_topk_prob, cfg.routed_scaling, ids, wts)
+            if topp > 0:        # expert top-p pruning: the tail moves to the top-1 expert with weight 0
+                from ..models.moe_policy import apply_topp
+                pi, pw = apply_topp(ids, wts, topp, self.ecfg.moet.topp_min)
+                ids.copy_(pi)
+                wts.copy_(pw)
             self._ensure_experts(mli, ids)
             if use_tc:
                 y2, posof = self._moe_tc(h2q, h2s, ids, ex, R, T, E_loc, e_lo)

@@ -49,6 +49,7 @@ class LLM:
                  delta_slots: int = 0, gate: Optional[bool] = None, expert_parallel: bool = False,
                  expert_store: str = "pinned", expert_store_dir: Optional[str] = None, **model_overrides):
         cfg = get_preset(model, **model_overrides) if isinstance(model, str) else model
+        self._mtp_requested = num_speculative_tokens > 0
         if num_layers is not None:
             cfg = cfg.replace(num_layers=num_layers)
         if device is None:
@@ -65,6 +66,9 @@ class LLM:
                                  kv_cache_dtype=kv_cache_dtype, num_speculative_tokens=num_speculative_tokens,
                                  cuda_graphs=cuda_graphs, seed=seed, device=str(self.device))
         self.tokenizer = ByteTokenizer(cfg.vocab)
+        if self.device.type == "cuda" and weights is None and not expert_cache_slots \
+                and self.ecfg.moet.base_cache_gb <= 0 and not self.ecfg.moet.force_resident:
+            self._resident_hardstop(cfg, tensor_parallel_size, expert_parallel, num_layers)
         self.expert_source = None
         if weights is None and self.ecfg.moet.planes_cache:
             # boot the expert planes from the persistent quantisation cache (first boot fills it)
@@ -118,6 +122,34 @@ class LLM:
             self.blocks = None
             self.runner = TorchRunner(self.mw, self.k, max_model_len, self.device)
 
+    def _resident_hardstop(self, cfg, tp, ep, num_layers):
+        """Refuse early when fully resident experts cannot fit beside a KV floor and
+        suggest a base-cache size instead (VLLM_MOE_W2_FORCE_RESIDENT=1 overrides)."""
+        from ..models.weights import ExpertLayout
+        from ..residency import resident_fit
+        L = (num_layers or cfg.num_layers) + (1 if self._mtp_requested else 0)
+        moe_layers = max(0, L - cfg.num_dense_layers)
+        I = cfg.moe_intermediate if ep else cfg.moe_intermediate // tp
+        E = cfg.num_experts // tp if ep else cfg.num_experts
+        need = moe_layers * E * ExpertLayout(H=cfg.hidden, I=I).slot_bytes
+        free, _ = torch.cuda.mem_get_info(self.device)
+        kv_floor = self.ecfg.max_model_len * self.ecfg.max_num_seqs * 1168 * (L + 1)
+        fits, gb = resident_fit(need, free, kv_floor)
+        if not fits:
+            raise MemoryError(f"routed experts need {need / 2**30:.1f} GiB resident but only {gb:.1f} GiB fit beside "
+                              f"the KV floor; set VLLM_MOE_W2_BASE_CACHE_GB (e.g. {max(1.0, 0.9 * gb):.0f}) to serve "
+                              "them through the expert cache, or VLLM_MOE_W2_FORCE_RESIDENT=1")
+
+    def shutdown(self):
+        """Stop the residency managers (tiers first), then release stores and peer buffers."""
+        for tier in (getattr(self, "delta", None), getattr(self, "cache", None)):
+            if tier is not None:
+                tier.close()
+                tier.store.release()
+        ar = getattr(getattr(self, "runner", None), "ar", None)
+        if ar is not None:
+            ar.close()
+
     def _attach_delta(self, slots, gate):
         """FP4 delta tier of `slots` hot experts (+ the confidence gate that fills it)."""
         from ..residency import ConfidenceGate, moe_layers
@@ -160,6 +192,12 @@ class LLM:
                 raise ValueError("pack / tiered expert stores need a store directory (VLLM_MOE_W2_STORE_DIR)")
         from ..utils.observability import KpiLogger
         self.kpi = KpiLogger(every=m.kpi_every)
+        from ..residency import moe_layers, working_set_floor
+        floor = working_set_floor(len(moe_layers(self.mw)), self.cfg.top_k, self.k, self.ecfg.max_num_seqs,
+                                  self.cfg.num_experts)
+        if slots < floor and not m.force_pool:
+            raise ValueError(f"expert cache of {slots} slots is below the working-set floor {floor} "
+                             "(one decode step's routed experts); raise it or set VLLM_MOE_W2_FORCE_POOL=1")
         self.cache = build_expert_cache(self.mw, slots, kind, self.device, **kw)
         self.runner.attach_expert_cache(self.cache)
         self.replay = ReplayEngine(self.cache, tp_group=tp_group, mode=m.replay_mode, fp_max=m.fp_max,

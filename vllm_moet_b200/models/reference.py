@@ -126,8 +126,20 @@ def _stable_topk(x: torch.Tensor, k: int) -> torch.Tensor:
     return perm[:, :k]
 
 
+_TOPP = (0.0, 1)
+
+
+def set_topp(p: float, min_keep: int = 1):
+    """Expert top-p pruning in the oracle (mirrors MoetConfig.topp)."""
+    global _TOPP
+    _TOPP = (p, min_keep)
+
+
 def moe_block(cfg: ModelConfig, lw: LayerWeights, h: torch.Tensor) -> torch.Tensor:
     ids, w = route(cfg, lw, h)
+    if _TOPP[0] > 0:
+        from .moe_policy import apply_topp
+        ids, w = apply_topp(ids, w, *_TOPP)
     out = torch.zeros_like(h, dtype=torch.float32)
     ex = lw.experts
     lo, n_loc = ex.e_lo, ex.n_local

@@ -278,10 +278,12 @@ class _null:
         return False
 
 
-def working_set_floor(moe_layers: int, top_k: int, spec_tokens: int, max_seqs: int) -> int:
+def working_set_floor(moe_layers: int, top_k: int, spec_tokens: int, max_seqs: int,
+                      num_experts: int = 1 << 30) -> int:
     """Slots a base pool needs so one decode step's routed pairs always fit
-    (moe layers x top_k x (1 + spec) x min(seqs, 4), with a 1.15 margin)."""
-    return int(1.15 * moe_layers * top_k * (1 + spec_tokens) * min(max_seqs, 4) + 0.999)
+    (moe layers x min(E, top_k x (1 + spec) x min(seqs, 4)), with a 1.15 margin)."""
+    per_layer = min(num_experts, top_k * (1 + spec_tokens) * min(max_seqs, 4))
+    return int(1.15 * moe_layers * per_layer + 0.999)
 
 
 def resident_fit(expert_bytes_total: int, free_bytes: int, kv_floor_bytes: int, reserve_bytes: int = 2 << 30):
