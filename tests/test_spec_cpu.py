@@ -64,3 +64,20 @@ def test_dspark_drafter_shapes():
     assert torch.allclose(probs.sum(-1), torch.ones(3, 4))
     w = allocate_widths(surv, torch.ones(4), num_reqs=3, length=4, tau=0.0, budget_frac=0.5)
     assert int(w.sum()) <= 6
+
+
+def test_dspark_swa_indices():
+    from vllm_moet_b200.spec import swa_indices
+    idx = swa_indices(context_len=1000, block_len=4, window=256)
+    assert idx.numel() == 512 and idx.numel() % 128 == 0
+    valid = idx[idx >= 0]
+    assert valid.tolist() == list(range(744, 1004))
+    big = swa_indices(context_len=5000, block_len=8, window=600)
+    assert big.numel() == 640 and int((big >= 0).sum()) == 608
+
+
+def test_quant_study_orders_formats():
+    import torch
+    from vllm_moet_b200.tools.quant_study import study
+    r = study(torch.randn(64, 256) * 0.02)
+    assert r["nvfp4"][0] < r["2-bit codebook (auto)"][0] and r["mxfp4 (delta tier)"][0] < r["2-bit codebook (auto)"][0]

@@ -86,3 +86,18 @@ class DSparkDrafter(nn.Module):
             drafts.append(prev)
             probs.append(p)
         return torch.stack(drafts, 1), torch.stack(probs, 1), surv
+
+
+def swa_indices(context_len: int, block_len: int, window: int, min_width: int = 512, align: int = 128) -> torch.Tensor:
+    """KV positions the DSpark draft block attends to (non-causal within the block):
+    the trailing ``window`` context positions plus every query position of the block
+    (future ones included), padded with -1 to a width >= ``min_width`` that is a
+    multiple of ``align`` (reference: DSpark SWA indices, patch P:17441-17617)."""
+    start = max(0, context_len - window)
+    ctx = torch.arange(start, context_len, dtype=torch.int32)
+    blk = torch.arange(context_len, context_len + block_len, dtype=torch.int32)
+    idx = torch.cat([ctx, blk])
+    width = max(min_width, -(-idx.numel() // align) * align)
+    out = torch.full((width,), -1, dtype=torch.int32)
+    out[: idx.numel()] = idx
+    return out
