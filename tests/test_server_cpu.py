@@ -101,3 +101,39 @@ def test_streaming_and_chat(server):
                                                           "max_tokens": 4, "ignore_eos": True}, timeout=120)
     assert r.ok and r.json()["choices"][0]["message"]["role"] == "assistant"
     assert requests.post(url + "/v1/completions", json={"prompt": "x", "temperature": 0.7}).status_code == 400
+
+
+def _tp_serving(rank, world):
+    """Rank 0 serves (EngineWorker batches broadcast to followers); rank 1 follows."""
+    import torch.distributed as dist
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    from vllm_moet_b200.entrypoints.openai_server import EngineWorker, follower_loop
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=128,
+              tensor_parallel_size=world, tp_group=dist.group.WORLD, tp_rank=rank)
+    if rank != 0:
+        follower_loop(llm, dist.group.WORLD)
+        return None
+    import threading
+    done = threading.Event()
+    got = {}
+
+    def cb(ids, finish):
+        got.setdefault("ids", []).extend(ids)
+        if finish:
+            done.set()
+    w = EngineWorker(llm, "tiny-moe", tp_group=dist.group.WORLD)
+    w.submit([5, 6, 7, 8], SamplingParams(max_tokens=6, ignore_eos=True), cb)
+    done.wait(120)
+    w.close()
+    return got["ids"]
+
+
+def test_tp2_serving_followers_match_single_rank():
+    from mp_util import run_ranks
+    from vllm_moet_b200.engine.llm import LLM
+    from vllm_moet_b200 import SamplingParams
+    ids = run_ranks(_tp_serving, 2)[0]
+    one = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=128)
+    want = one.generate([[5, 6, 7, 8]], SamplingParams(max_tokens=6, ignore_eos=True))[0].outputs[0].token_ids
+    assert ids == want

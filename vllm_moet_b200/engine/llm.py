@@ -120,7 +120,7 @@ class LLM:
         else:
             from .torch_runner import TorchRunner
             self.blocks = None
-            self.runner = TorchRunner(self.mw, self.k, max_model_len, self.device)
+            self.runner = TorchRunner(self.mw, self.k, max_model_len, self.device, tp_group=tp_group)
 
     def _resident_hardstop(self, cfg, tp, ep, num_layers):
         """Refuse early when fully resident experts cannot fit beside a KV floor and

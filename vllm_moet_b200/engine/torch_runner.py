@@ -11,18 +11,27 @@ from ..models.weights import ModelWeights
 
 
 class TorchRunner:
-    def __init__(self, mw: ModelWeights, k: int, max_len: int, device="cpu"):
+    def __init__(self, mw: ModelWeights, k: int, max_len: int, device="cpu", tp_group=None):
         self.mw = mw
         self.k = k if mw.mtp is not None else 0
         self.dev = torch.device(device)
         self.cs = ref.rope_cos_sin(mw.cfg, max_len + 64, self.dev)
         self.rows = {}
+        self.tp_group = tp_group        # tensor-parallel CPU ranks (gloo): sharded weights, all-reduced partials
 
     def _row(self, r):
         return self.rows[r]
 
+    def _ctx(self):
+        import contextlib
+        return ref.tp_context(self.tp_group) if self.tp_group is not None else contextlib.nullcontext()
+
     @torch.no_grad()
     def prefill(self, prompts, rows):
+        with self._ctx():
+            return self._prefill(prompts, rows)
+
+    def _prefill(self, prompts, rows):
         firsts = []
         for prompt, r in zip(prompts, rows):
             n = len(prompt)
@@ -47,6 +56,10 @@ class TorchRunner:
     @torch.no_grad()
     def step(self, rows):
         """-> {row: (emitted tokens list, n_accepted)}"""
+        with self._ctx():
+            return self._step(rows)
+
+    def _step(self, rows):
         out = {}
         k = self.k
         for r in rows:
