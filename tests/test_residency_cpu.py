@@ -260,3 +260,25 @@ def test_prefetchers(tmp_path):
 
 def test_floor_caps_at_expert_count():
     assert working_set_floor(3, 4, 2, 2, num_experts=16) == int(1.15 * 3 * 16 + 0.999)
+
+
+def _pp_gate(rank, world, fail_rank):
+    import torch.distributed as dist
+    from vllm_moet_b200.residency import FetchError, pp_gate_barrier
+    calls = []
+
+    def promote():
+        calls.append(rank)
+        if rank == fail_rank:
+            raise FetchError("injected promotion failure")
+    # only the last stage's vote counts
+    fire = (rank == world - 1)
+    out = pp_gate_barrier(fire, promote, pp_group=dist.group.WORLD)
+    return out, calls
+
+
+def test_pp_gate_barrier_consensus_and_fail_closed():
+    res = run_ranks(_pp_gate, 3, -1)
+    assert all(o for o, _ in res) and all(c for _, c in res)     # every stage promoted and replays
+    res = run_ranks(_pp_gate, 3, 1)
+    assert not any(o for o, _ in res)                             # one failure -> nobody replays

@@ -238,3 +238,29 @@ def gate_fire_floor(moe_layers: int, top_k: int, rows: int, fp_max: int) -> int:
     """Slots an FP4 gate pool needs: one fire promotes every routed expert of the
     step, and each replay round can route to new ones (growth 1 + 0.35 (fp_max - 1))."""
     return int(math.ceil(moe_layers * top_k * rows * (1 + 0.35 * (fp_max - 1))))
+
+
+def pp_gate_barrier(fire_on_last: bool, promote, tp_group=None, pp_group=None, device="cpu") -> bool:
+    """Pipeline-parallel gate consensus (reference: ``_gate_pp_barrier``, patch
+    P:22083-22164).  The last PP stage decides whether the confidence gate fires;
+    the decision is broadcast to every stage; every rank then promotes its own
+    layers' experts and the outcome is agreed fail-closed (MIN over the TP group,
+    then over the PP group).  Returns True only when every rank promoted, i.e.
+    when the whole pipeline must re-run the step."""
+    import torch.distributed as dist
+    flag = torch.tensor([1 if fire_on_last else 0], dtype=torch.int32, device=device)
+    if pp_group is not None:
+        last = dist.get_global_rank(pp_group, dist.get_world_size(pp_group) - 1)
+        dist.broadcast(flag, src=last, group=pp_group)
+    if not int(flag.item()):
+        return False
+    ok = 1
+    try:
+        promote()
+    except FetchError:
+        ok = 0
+    t = torch.tensor([ok], dtype=torch.int32, device=device)
+    for g in (tp_group, pp_group):
+        if g is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MIN, group=g)
+    return bool(int(t.item()))
