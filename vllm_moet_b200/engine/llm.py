@@ -140,6 +140,11 @@ class LLM:
                               f"the KV floor; set VLLM_MOE_W2_BASE_CACHE_GB (e.g. {max(1.0, 0.9 * gb):.0f}) to serve "
                               "them through the expert cache, or VLLM_MOE_W2_FORCE_RESIDENT=1")
 
+    def reload_weights(self, *a, **k):
+        """Weight updates are refused on the 2-bit expert path: the expert planes,
+        their caches and the captured graphs derive from the loaded weights."""
+        raise NotImplementedError("reload_weights is not supported with 2-bit experts; build a new LLM")
+
     def shutdown(self):
         """Stop the residency managers (tiers first), then release stores and peer buffers."""
         for tier in (getattr(self, "delta", None), getattr(self, "cache", None)):
