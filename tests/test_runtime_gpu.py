@@ -108,3 +108,18 @@ def test_indexer_engine(llm):
                  max_model_len=1024, max_num_seqs=4)
     a = sparse.generate(p, sp)[0].outputs[0].token_ids
     assert a == sparse.generate(p, sp)[0].outputs[0].token_ids and len(a) == 8
+
+
+@pytest.mark.parametrize("tp,ep", [(4, False), (8, False), (8, True)])
+def test_tp_shard_shapes_run_on_one_gpu(tp, ep):
+    """Rank 0's shards of a TP4 / TP8 DS4-dims model (4 or 8 heads, expert shards of
+    384 / 192 rows, padded FFN shards, a vocab slice) run through every prefill and
+    decode kernel on one GPU (no group: partial sums are not reduced, so only the
+    shape paths are checked)."""
+    from vllm_moet_b200.config import ds4_flash_config
+    cfg = ds4_flash_config(num_layers=2, num_experts=16, vocab=4096)
+    llm = LLM(cfg, device="cuda", num_speculative_tokens=2, max_model_len=1024, max_num_seqs=2,
+              tensor_parallel_size=tp, tp_rank=0, expert_parallel=ep)
+    out = llm.generate([_prompt(300, 5)], SamplingParams(max_tokens=6, ignore_eos=True))
+    assert len(out[0].outputs[0].token_ids) == 6
+    llm.runner.check_status("tp shard shapes")
