@@ -158,7 +158,36 @@ MOET_DEVICE uint32_t f32x8_to_e2m1x8(const float* f) {
 }  // namespace moet
 
 #include <cstdlib>
+#include <mutex>
+#include <unordered_set>
 #include <utility>
+// Host: allow a kernel the device's whole opt-in dynamic shared memory, once per
+// kernel.  The attribute is per function, not per launch: setting it to each
+// launch's own size would leave it at the LAST size, and a CUDA-graph node
+// captured earlier with a larger size is then over the limit whenever the node is
+// launched on its own.  The attribute is a ceiling only; occupancy follows the
+// size each launch requests.
+inline void moet_allow_max_smem(const void* kern) {
+  static std::mutex mu;
+  static std::unordered_set<const void*> done;
+  static int optin = 0;
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count(kern)) return;
+  if (!optin) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  }
+  int static_bytes = 0;
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess) static_bytes = (int)fa.sharedSizeBytes;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - static_bytes);
+  done.insert(kern);
+}
+template <typename... KArgs>
+inline void moet_allow_max_smem(void (*kern)(KArgs...)) {
+  moet_allow_max_smem(reinterpret_cast<const void*>(kern));
+}
 // Host: launch with the programmatic-stream-serialization attribute (PDL) unless
 // MOET_PDL=0.  Captured into CUDA graphs as programmatic dependency edges.
 inline bool moet_pdl_enabled() {

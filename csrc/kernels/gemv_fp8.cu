@@ -201,8 +201,7 @@ void gemv_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor w, torch::Tensor 
     const int nwarps = std::max(1, std::min(8, (nchunks + U - 1) / U));
     dim3 grid((N + 15) / 16, (T + 8 * NT - 1) / (8 * NT), B);
     size_t smem = nwarps > 1 ? (size_t)nwarps * NT * 4 * 32 * sizeof(float) : 0;
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(gemv_fp8_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (smem > 48 * 1024) moet_allow_max_smem(gemv_fp8_kernel<NT>);
     cudaFuncSetAttribute(gemv_fp8_kernel<NT>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     launch_k(gemv_fp8_kernel<NT>, grid, nwarps * 32, smem, stream, p);
   };

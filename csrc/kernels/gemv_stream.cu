@@ -304,7 +304,7 @@ void gemv_stream_fp8(c10::optional<torch::Tensor> a_opt, c10::optional<torch::Te
   static int n_sm = 0;
   if (!n_sm) cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, 0);
   const int nblocks = (N + gs::kRows - 1) / gs::kRows;
-  cudaFuncSetAttribute(gemv_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  moet_allow_max_smem(gemv_stream_kernel);
   auto stream = at::cuda::getCurrentCUDAStream();
   launch_k(gemv_stream_kernel, std::min(nblocks, n_sm), gs::kWarps * 32, smem, stream, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -544,13 +544,13 @@ void mla_decode(torch::Tensor q, torch::Tensor kv, torch::Tensor block_table, to
     const int MT = 1;
     size_t smem = (size_t)((nv4 ? 1 : 2) * kBS * kRow + 16 * MT * kRow + 16 * MT * kPRow) * 2 + 8 * 16 * MT * 4 + 16 +
                   (nv4 ? 2 * kBlockBytes4 : 0);
-    cudaFuncSetAttribute(mla_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    moet_allow_max_smem(mla_decode_kernel<1>);
     launch_k(mla_decode_kernel<1>, grid, 256, smem, stream, p);
   } else {
     const int MT = 2;
     size_t smem = (size_t)((nv4 ? 1 : 2) * kBS * kRow + 16 * MT * kRow + 16 * MT * kPRow) * 2 + 8 * 16 * MT * 4 + 16 +
                   (nv4 ? 2 * kBlockBytes4 : 0);
-    cudaFuncSetAttribute(mla_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    moet_allow_max_smem(mla_decode_kernel<2>);
     launch_k(mla_decode_kernel<2>, grid, 256, smem, stream, p);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -238,7 +238,7 @@ void mla_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kr, torch::Te
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.out_q = (uint8_t*)opt_ptr(out_q); p.out_s = (uint8_t*)opt_ptr(out_s); p.out_bf16 = (__nv_bfloat16*)opt_ptr(out_bf16);
   const size_t smem = (size_t)(2 * kBK * kKS + 2 * kBK * kVS + kBQ * kKS) * 2;
-  cudaFuncSetAttribute(mla_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  moet_allow_max_smem(mla_prefill_kernel);
   auto stream = at::cuda::getCurrentCUDAStream();
   dim3 grid((max_len + kBQ - 1) / kBQ, Hh, nseq);
   mla_prefill_kernel<<<grid, 256, smem, stream>>>(p);

@@ -444,7 +444,7 @@ void moe_route_fused(torch::Tensor x, torch::Tensor w, torch::Tensor logits, c10
   auto stream = at::cuda::getCurrentCUDAStream();
   const size_t smem = (size_t)4 * H * 2;
   // static shared memory of the top-k / pair-list phases + the token stage exceed the 48 KiB default
-  cudaFuncSetAttribute(moe_route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  moet_allow_max_smem(moe_route_fused_kernel);
   launch_k(moe_route_fused_kernel, (E + kRouteExperts - 1) / kRouteExperts, kRouteWarps * 32, smem, stream,
            (const __nv_bfloat16*)x.data_ptr(), T, H, (const __nv_bfloat16*)w.data_ptr(), E, logits.data_ptr<float>(),
            bias.has_value() && bias->defined() ? (const float*)bias->data_ptr<float>() : (const float*)nullptr,

@@ -55,7 +55,7 @@ struct TcSmem {
 template <int NT, int ASRC>
 __global__ void __launch_bounds__(128) tc_gemm_kernel(TcArgs p) {
   extern __shared__ __align__(1024) uint8_t sm[];
-  __shared__ uint64_t bars[kBufs + 1];
+  __shared__ uint64_t bars[kBufs + 2];   // stage buffers, accumulator done, drain
   __shared__ uint32_t taddr_s;
   using L = TcSmem<NT>;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(128) tc_gemm_kernel(TcArgs p) {
   const int nstages = K / kStageK;
 
   if (warp == 0) tc::tmem_alloc(&taddr_s, L::TMEM_COLS);
-  if (tid == 0) { for (int i = 0; i <= kBufs; i++) tc::mbar_init(&bars[i], 1); }
+  if (tid == 0) { for (int i = 0; i <= kBufs + 1; i++) tc::mbar_init(&bars[i], 1); }
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
@@ -224,7 +224,12 @@ __global__ void __launch_bounds__(128) tc_gemm_kernel(TcArgs p) {
   }
   if (ok) ok = tc::mbar_wait(&bars[kBufs], 0);
   if (!__syncthreads_and(ok)) {
-    if (tid == 0) set_status(p.status, kTimeout);
+    if (tid == 0) {
+      set_status(p.status, kTimeout);
+      // drain: a commit tracks every MMA this thread issued; wait (bounded) before TMEM is freed
+      tc::commit(&bars[kBufs + 1]);
+      tc::mbar_wait(&bars[kBufs + 1], 0);
+    }
   } else {
     tc::fence_after();
     const int row = warp * 32 + lane;
@@ -256,7 +261,7 @@ __global__ void __launch_bounds__(128) tc_gemm_kernel(TcArgs p) {
 template <int NT, int ASRC>
 static void launch_tc(const TcArgs& a, dim3 grid, cudaStream_t stream) {
   using L = TcSmem<NT>;
-  cudaFuncSetAttribute(tc_gemm_kernel<NT, ASRC>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+  moet_allow_max_smem(tc_gemm_kernel<NT, ASRC>);
   // ask for the full shared-memory carveout so several CTAs share an SM
   cudaFuncSetAttribute(tc_gemm_kernel<NT, ASRC>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   tc_gemm_kernel<NT, ASRC><<<grid, 128, L::TOTAL, stream>>>(a);

@@ -76,7 +76,7 @@ void tc_gemm_test(torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch::Ten
   TORCH_CHECK(a.size(0) == 128 && K % 128 == 0 && K <= 512 && N >= 1 && N <= 128, "tc_gemm_test shape (one 128-row scale atom: N <= 128)");
   const size_t smem = 128 * K + ((N + 7) / 8) * 8 * K + 2 * (K / 128) * 512;
   TORCH_CHECK(smem <= 200 * 1024, "tc_gemm_test: smem");
-  cudaFuncSetAttribute(tc_gemm_test_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  moet_allow_max_smem(tc_gemm_test_kernel);
   auto stream = at::cuda::getCurrentCUDAStream();
   tc_gemm_test_kernel<<<1, 128, smem, stream>>>((const uint8_t*)a.data_ptr(), (const uint8_t*)sa.data_ptr(),
                                                 (const uint8_t*)b.data_ptr(), (const uint8_t*)sb.data_ptr(), N, K,

@@ -99,7 +99,7 @@ __global__ void __launch_bounds__(64 + kConvThreads, 1) tc_ws_kernel(const __gri
   const int G = p.act_groups;                              // scale bytes per token row
   uint8_t* tsc = sm + S * Cf::STAGE;                        // [2][NT][G] token scale rows (per tile)
   uint8_t* tsw = tsc + 2 * NT * G;                          // [K/128] dense weight scales of the tile row block
-  __shared__ uint64_t full[S], conv[S], empty[S], accfull[2], accempty[2], tfull[2], tempty[2];
+  __shared__ uint64_t full[S], conv[S], empty[S], accfull[2], accempty[2], tfull[2], tempty[2], drain;
   __shared__ uint32_t taddr_s;
   __shared__ volatile int err_s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(64 + kConvThreads, 1) tc_ws_kernel(const __gri
       tc::mbar_init(&accfull[i], 1); tc::mbar_init(&accempty[i], kConvWarps);
       tc::mbar_init(&tfull[i], 1); tc::mbar_init(&tempty[i], kConvWarps);
     }
+    tc::mbar_init(&drain, 1);
     err_s = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -143,11 +144,14 @@ __global__ void __launch_bounds__(64 + kConvThreads, 1) tc_ws_kernel(const __gri
     // ------------------------------------------------------------ producer (lane 0)
     if (lane == 0) {
       int st = 0; uint32_t ph = 0; int tb = 0; uint32_t tph = 0;
+      uint32_t issued = 0, tissued = 0;           // bit i: slot i has a fill in flight or landed, parity in *_ph
+      uint32_t issued_ph = 0, tissued_ph = 0;
       long long t0 = clock64(), tw = 0;
       for (int tile = blockIdx.x; tile < ntiles && !*err; tile += gridDim.x) {
         int m0, r0, nrows, slot;
         if (!tile_info(tile, m0, r0, nrows, slot)) continue;
         if (!ws::wait(&tempty[tb], tph ^ 1, err, tw)) break;
+        tissued |= 1u << tb; tissued_ph = (tissued_ph & ~(1u << tb)) | (tph << tb);
         ws::mbar_expect_tx(&tfull[tb], NT * G);
         ws::bulk_g2s(tsc + tb * NT * G, p.act_s + (size_t)r0 * G, NT * G, &tfull[tb]);
         if (++tb == 2) { tb = 0; tph ^= 1; }
@@ -163,8 +167,15 @@ __global__ void __launch_bounds__(64 + kConvThreads, 1) tc_ws_kernel(const __gri
             ws::tma_4d(sA, &map_w, 0, 0, s * 8, m0 / 8, &full[st]);
           }
           ws::tma_4d(sB, &map_b, 0, 0, s * 8, r0 / 8, &full[st]);
+          issued |= 1u << st; issued_ph = (issued_ph & ~(1u << st)) | (ph << st);
           if (++st == S) { st = 0; ph ^= 1; }
         }
+      }
+      if (*err) {   // a wait gave up: let every copy this thread started land before the CTA exits
+        for (int i = 0; i < S; i++)
+          if (issued >> i & 1) tc::mbar_wait(&full[i], issued_ph >> i & 1);
+        for (int i = 0; i < 2; i++)
+          if (tissued >> i & 1) tc::mbar_wait(&tfull[i], tissued_ph >> i & 1);
       }
       if (p.dbg_clk && blockIdx.x == 0) { p.dbg_clk[0] = clock64() - t0; p.dbg_clk[1] = tw; }
     }
@@ -201,6 +212,10 @@ __global__ void __launch_bounds__(64 + kConvThreads, 1) tc_ws_kernel(const __gri
         }
         tc::commit(&accfull[acc]);
         if (++acc == 2) { acc = 0; aph ^= 1; }
+      }
+      if (*err) {   // a wait gave up: a commit tracks every MMA issued so far; wait for them before TMEM is freed
+        tc::commit(&drain);
+        tc::mbar_wait(&drain, 0);
       }
       if (p.dbg_clk && blockIdx.x == 0) { p.dbg_clk[2] = clock64() - t0; p.dbg_clk[3] = tw; p.dbg_clk[4] = twa; }
     }
@@ -361,7 +376,7 @@ static void launch_ws(const WsArgs& a, const CUtensorMap& mw, const CUtensorMap&
   if (!sms) { int dev; cudaGetDevice(&dev); cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev); }
   const int smem = Cf::S * Cf::STAGE + 2 * NT * a.act_groups + 256 + 1024;
   TORCH_CHECK(smem <= 227 * 1024, "tc_ws: shared memory budget exceeded (", smem, " bytes)");
-  cudaFuncSetAttribute(tc_ws_kernel<NT, ASRC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  moet_allow_max_smem(tc_ws_kernel<NT, ASRC>);
   tc_ws_kernel<NT, ASRC><<<sms, 64 + kConvThreads, smem, stream>>>(mw, ms, mb, a);
 }
 

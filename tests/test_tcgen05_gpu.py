@@ -141,7 +141,8 @@ def test_ws_moe_w2_padded(C, T, k, E, N, K, NT):
             assert rel(got, A[tt] @ W.t()) < 1e-4, (tt, j)
 
 
-@pytest.mark.parametrize("T,N,K", [(1, 128, 128), (130, 384, 512), (300, 200, 1024), (256, 4096, 4096)])
+@pytest.mark.parametrize("T,N,K", [(1, 128, 128), (130, 384, 512), (300, 200, 1024), (256, 4096, 4096),
+                                   (96, 2112, 4096), (96, 4096, 11008)])
 def test_ws_gemm_fp8(C, T, N, K):
     g = torch.Generator().manual_seed(T + N + K)
     Tp = (T + 127) // 128 * 128

@@ -128,6 +128,8 @@ class NativeRunner:
         self.debug_finite = os.environ.get("MOET_DEBUG_FINITE", "0") == "1"
         self.branches = os.environ.get("MOET_BRANCHES", "1") != "0"
         self.gemv_stream = os.environ.get("MOET_GEMV_STREAM", "1") != "0"
+        # token count from which dense linears run on the tcgen05 GEMM (128-token tiles)
+        self.tc_min_t = int(os.environ.get("MOET_TC_MIN_T", "16"))
 
     # ------------------------------------------------------------------ helpers
     @staticmethod
@@ -137,7 +139,7 @@ class NativeRunner:
     def _fp8(self, name, T, K):
         """FP8 activation buffers; rows are allocated in multiples of 128 so the
         tensor-core GEMM can read whole 128-row TMA boxes (callers see [:T])."""
-        Tp = self._pad128(T) if T > 128 else T
+        Tp = self._pad128(T) if T >= self.tc_min_t else T
         q = self.ws.get(name + ".q", (Tp, K), torch.uint8)
         s = self.ws.get(name + ".s", (Tp, K // 64), torch.uint8)
         return q[:T], s[:T]
@@ -157,7 +159,7 @@ class NativeRunner:
         token counts, the weight-streaming GEMV for decode-sized ones."""
         T, K = aq.shape[0], lin.w.shape[-1]
         N = lin.w.shape[0]
-        if T > 128 and K % 128 == 0 and lin.w.dim() == 2 and N % 8 == 0:
+        if T >= self.tc_min_t and K % 128 == 0 and lin.w.dim() == 2 and N % 8 == 0:
             Tp = self._pad128(T)
             ap, sp = self._padded_view(aq, Tp), self._padded_view(as_, Tp)
             if ap is not None and sp is not None:
