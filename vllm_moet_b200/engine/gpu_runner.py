@@ -130,6 +130,10 @@ class NativeRunner:
         self.gemv_stream = os.environ.get("MOET_GEMV_STREAM", "1") != "0"
         # token count from which dense linears run on the tcgen05 GEMM (128-token tiles)
         self.tc_min_t = int(os.environ.get("MOET_TC_MIN_T", "16"))
+        # decode expert tiles: 8-token pairs up to this many routed rows, 16-token pairs above
+        self.mb8_max_r = int(os.environ.get("MOET_MB8_MAX_R", "2048"))
+        # decode experts on the tcgen05 kernel with this token tile (0: mma.sync GEMV)
+        self.decode_tc_nt = int(os.environ.get("MOET_DECODE_TC_NT", "0"))
 
     # ------------------------------------------------------------------ helpers
     @staticmethod
@@ -481,6 +485,9 @@ class NativeRunner:
             self._ensure_experts(mli, ids)
             if use_tc:
                 y2, posof = self._moe_tc(h2q, h2s, ids, ex, R, T, E_loc, e_lo)
+            elif (self.decode_tc_nt and ctx.mode == "decode" and H % 128 == 0 and I % 128 == 0
+                  and self.delta is None):
+                y2, posof = self._moe_tc(h2q, h2s, ids, ex, R, T, E_loc, e_lo, MB=self.decode_tc_nt)
             else:
                 y2, posof = self._moe_gemv(h2q, h2s, ids, ex, R, ctx.mb, mli, E_loc, e_lo)
         if sh is not None:
@@ -499,14 +506,13 @@ class NativeRunner:
             else:
                 torch.add(x, part, out=out)
 
-    def _moe_tc(self, h2q, h2s, ids, ex, R, T, E=None, e_lo=-1):
+    def _moe_tc(self, h2q, h2s, ids, ex, R, T, E=None, e_lo=-1, MB=128):
         """Prefill experts on tensor cores: 128-row expert-aligned pairs, activations
         gathered into expert order, two warp-specialized tcgen05 GEMMs."""
         C, cfg = self.C, self.cfg
         E, H = E or cfg.num_experts, cfg.hidden
         L = ex.layout
         I = L.I
-        MB = 128
         P = R // MB + min(E, R)
         Rp = P * MB
         rank = self.ws.get("rank", (R,), torch.int32)
@@ -739,7 +745,7 @@ class NativeRunner:
         slot = blk.long() * KV_BLOCK + (pos % KV_BLOCK).long()
         slot = torch.where(st.active_rows, slot, torch.full_like(slot, -1))
         ctx = StepCtx(T=T, pos=pos.int(), seq=st.seq_rows, slot=slot, block_table=st.block_table, mode="decode",
-                      mb=8 if T * self.cfg.top_k <= 256 else 16)
+                      mb=8 if T * self.cfg.top_k <= self.mb8_max_r else 16)
         x = self._main(st.tokens.view(-1), ctx)
         if not self.last_stage:
             self._pp_broadcast_state(st)
