@@ -2,6 +2,7 @@
 
     python -m vllm_moet_b200.entrypoints.openai_server --model ds4-flash-shape --port 8000
     torchrun --nproc-per-node 8 -m vllm_moet_b200.entrypoints.openai_server --model ds4-flash-shape
+    python -m vllm_moet_b200.entrypoints.openai_server --data-parallel-size 4 --tensor-parallel-size 2
 
 Endpoints: ``GET /health``, ``GET /v1/models``, ``POST /v1/completions``,
 ``POST /v1/chat/completions`` (DeepSeek-V4 chat encoding, ``reasoning_effort``,
@@ -248,11 +249,24 @@ def main(argv=None):
     ap.add_argument("--max-num-seqs", type=int, default=32)
     ap.add_argument("--num-speculative-tokens", type=int, default=2)
     ap.add_argument("--device", default=None)
+    ap.add_argument("--data-parallel-size", type=int, default=1,
+                    help="replicated engines behind a request router (see dp_serve)")
+    ap.add_argument("--tensor-parallel-size", type=int, default=None,
+                    help="GPUs per replica with --data-parallel-size; otherwise torchrun's WORLD_SIZE")
+    ap.add_argument("--gpus", default=None, help="GPU ids for the replicas of --data-parallel-size ('cpu': none)")
     args = ap.parse_args(argv)
+    if args.data_parallel_size > 1:
+        import sys
+        from .dp_serve import main as dp_main
+        dp_main(list(sys.argv[1:] if argv is None else argv))
+        return
     import torch
     from ..engine.llm import LLM
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.tensor_parallel_size not in (None, world):
+        raise SystemExit(f"--tensor-parallel-size {args.tensor_parallel_size} without --data-parallel-size: "
+                         f"launch with torchrun --nproc-per-node {args.tensor_parallel_size}")
     group = None
     if world > 1:
         import torch.distributed as dist
