@@ -44,7 +44,7 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
                  torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
                  torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
                  c10::optional<torch::Tensor> miss_count, c10::optional<torch::Tensor> pool8, int64_t codes_off8,
-                 int64_t scale_off8, c10::optional<torch::Tensor> slot_table8);
+                 int64_t scale_off8, c10::optional<torch::Tensor> slot_table8, bool quintal);
 void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::optional<torch::Tensor> resid,
                  c10::optional<torch::Tensor> shared_out, c10::optional<torch::Tensor> out,
                  c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> ar);
@@ -158,7 +158,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("n_pairs"), py::arg("pool"), py::arg("codes_off"), py::arg("scale_off"), py::arg("slot_table"),
         py::arg("out"), py::arg("N"), py::arg("K"), py::arg("rows_per_pair"), py::arg("miss_count"),
         py::arg("pool8") = py::none(), py::arg("codes_off8") = 0, py::arg("scale_off8") = 0,
-        py::arg("slot_table8") = py::none());
+        py::arg("slot_table8") = py::none(), py::arg("quintal") = false);
   m.def("moe_combine", &moe_combine, py::arg("y"), py::arg("pos_of"), py::arg("wts"), py::arg("resid"),
         py::arg("shared_out"), py::arg("out"), py::arg("out_f32"), py::arg("ar") = py::none());
   m.def("bf12_decode", &bf12_decode);

@@ -19,6 +19,14 @@
 //   block scale (an exact power of two) and the activation scale are applied
 //   with FMAs, exactly as the format defines the dequantised weight.
 // * Misses (slot < 0) write zero rows and bump a miss counter.
+// * Delta tier, two containers.  Direct-8: the slot holds e4m3 bytes already in
+//   A-fragment register order (no decode).  Split FP4 ("quintal", w4q): the slot
+//   holds only a radix-5 refinement plane read against the resident 2-bit base
+//   (codes and scales of the base slot); per group of 4 codes a 10-bit word gives
+//   the e2m1 magnitude index inside each code's class ({0,.5,1,1.5,2} or
+//   {3,4,6}), so the decode rebuilds the exact MXFP4 value: digits from a
+//   per-warp 625-entry table, class offset from the code bits, one prmt over the
+//   e2m1 -> e4m3 magnitude pool, the sign bit from the base level.
 #include "common.cuh"
 #include "symm.cuh"
 #include "torch_glue.h"
@@ -38,7 +46,27 @@ struct W2Args {
   // scales); an expert with a delta slot >= 0 is served from it instead of the 2-bit slot
   const uint8_t* pool8; long long slot_bytes8, codes_off8, scale_off8;
   const int* slot_table8;
+  int quintal;                  // delta slots hold split-FP4 refinement planes (base codes + scales stay in use)
 };
+
+// 10-bit quintal word -> (d0 | d2 << 4) | (d1 | d3 << 4) << 8; x / 5 = (x * 0x334) >> 12 for x < 1024
+MOET_DEVICE uint32_t quintal_digit_word(uint32_t w) {
+  const uint32_t q1 = (w * 0x334u) >> 12, d0 = w - 5u * q1;
+  const uint32_t q2 = (q1 * 0x334u) >> 12, d1 = q1 - 5u * q2;
+  const uint32_t q3 = (q2 * 0x334u) >> 12, d2 = q2 - 5u * q3;
+  return (d0 | (d2 << 4)) | ((d1 | (q3 << 4)) << 8);
+}
+
+// One A-fragment register of split FP4: csel = the 4 code nibbles of the register (as the
+// 2-bit decode selects them), Ta / Tb = the digit words of its two groups, mode picks the
+// even (0x0040) or odd (0x0051) code positions.
+MOET_DEVICE uint32_t quintal_reg(uint32_t csel, uint32_t Ta, uint32_t Tb, uint32_t mode) {
+  constexpr uint32_t L = 0x4838B8C8u, MLO = 0x3C383000u, MHI = 0x4C484440u;
+  const uint32_t base = prmt(L, L, csel);
+  const uint32_t dsel = prmt(Ta, Tb, mode);
+  const uint32_t big = ~(csel ^ (csel >> 1)) & 0x1111u;      // codes 0 and 3: the {3, 4, 6} class
+  return prmt(MLO, MHI, dsel + 5u * big) | (base & 0x80808080u);
+}
 
 template <int NT>
 __global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Args p) {
@@ -51,7 +79,8 @@ __global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Arg
   const int nb = blockIdx.x * (blockDim.x >> 5) + warp;  // 16-row block
   if (nb * 16 >= p.N) return;
   const int slot8 = p.slot_table8 ? p.slot_table8[e] : -1;
-  const int slot = slot8 >= 0 ? slot8 : p.slot_table[e];
+  const bool split = p.quintal && slot8 >= 0;                 // refinement over the base: the base must be resident
+  const int slot = slot8 >= 0 && !p.quintal ? slot8 : p.slot_table[e];
   if (slot < 0) {
     if (blockIdx.x == 0 && threadIdx.x == 0 && p.miss_count) atomicAdd(p.miss_count, 1);
     for (int j = 0; j < nrows; j++)
@@ -59,11 +88,12 @@ __global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Arg
     return;
   }
   const int KC = p.K >> 6, KS = p.K >> 5;
-  const bool direct = slot8 >= 0;
+  const bool direct = slot8 >= 0 && !p.quintal;
   const uint8_t* base = direct ? p.pool8 + (size_t)slot8 * p.slot_bytes8 : p.pool + (size_t)slot * p.slot_bytes;
   const uint8_t* codes = direct ? base + p.codes_off8 + (size_t)nb * KC * 1024 + lane * 32
                                 : base + p.codes_off + (size_t)nb * KC * 256 + lane * 8;
   const uint8_t* sc = base + (direct ? p.scale_off8 : p.scale_off) + (size_t)nb * KS * 16;
+  const uint8_t* qrec = split ? p.pool8 + (size_t)slot8 * p.slot_bytes8 + p.codes_off8 + (size_t)nb * KC * 320 : nullptr;
 
   // activation row of sorted row r0 + j (gathered through the token map for w13)
   auto act_row = [&](int j) -> int {
@@ -88,6 +118,10 @@ __global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Arg
   uint8_t* ss = scale_smem + warp * 16 * KS;
   for (int i = lane; i < KS; i += 32)
     reinterpret_cast<uint4*>(ss)[i] = __ldg(reinterpret_cast<const uint4*>(sc) + i);
+  // split FP4: this warp's digit table (after every warp's scale stage: (blockDim/32) * 16 * KS bytes)
+  uint16_t* qlut = reinterpret_cast<uint16_t*>(scale_smem + (blockDim.x >> 5) * 16 * KS) + warp * 640;
+  if (split)
+    for (int w = lane; w < 625; w += 32) qlut[w] = (uint16_t)quintal_digit_word(w);
   __syncwarp();
 
   // Chunks are streamed in batches of U: all code loads of a batch are issued
@@ -134,6 +168,43 @@ __global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Arg
         if (c0 + u >= KC) break;
         const uint32_t A0[4] = {w0[u].x, w0[u].y, w0[u].z, w0[u].w};
         const uint32_t A1[4] = {w1[u].x, w1[u].y, w1[u].z, w1[u].w};
+        mma_chunk(c0 + u, A0, A1);
+      }
+    }
+  } else if (split) {
+    constexpr int UQ = 2;
+    for (int c0 = 0; c0 < KC; c0 += UQ) {
+      uint2 wv[UQ], qv[UQ];
+      uint32_t qh[UQ];
+#pragma unroll
+      for (int u = 0; u < UQ; u++)
+        if (c0 + u < KC) {
+          wv[u] = ldg_stream_u2(codes + (size_t)(c0 + u) * 256);
+          qv[u] = ldg_stream_u2(qrec + (size_t)(c0 + u) * 320 + lane * 8);
+          qh[u] = __ldg(reinterpret_cast<const unsigned short*>(qrec + (size_t)(c0 + u) * 320 + 256 + lane * 2));
+        }
+#pragma unroll
+      for (int u = 0; u < UQ; u++) {
+        if (c0 + u >= KC) break;
+        const uint32_t lo = wv[u].x, hi = wv[u].y, r0 = qv[u].x, r1 = qv[u].y, h = qh[u];
+        // the lane's 8 ten-bit words (80-bit little-endian record), one per group of 4 codes
+        uint32_t T[8];
+        T[0] = qlut[r0 & 0x3FFu];
+        T[1] = qlut[(r0 >> 10) & 0x3FFu];
+        T[2] = qlut[(r0 >> 20) & 0x3FFu];
+        T[3] = qlut[__funnelshift_r(r0, r1, 30) & 0x3FFu];
+        T[4] = qlut[(r1 >> 8) & 0x3FFu];
+        T[5] = qlut[(r1 >> 18) & 0x3FFu];
+        T[6] = qlut[__funnelshift_r(r1, h, 28) & 0x3FFu];
+        T[7] = qlut[(h >> 6) & 0x3FFu];
+        const uint32_t A0[4] = {quintal_reg(lo & 0x3333u, T[0], T[1], 0x0040u),
+                                quintal_reg(hi & 0x3333u, T[4], T[5], 0x0040u),
+                                quintal_reg((lo >> 2) & 0x3333u, T[0], T[1], 0x0051u),
+                                quintal_reg((hi >> 2) & 0x3333u, T[4], T[5], 0x0051u)};
+        const uint32_t A1[4] = {quintal_reg((lo >> 16) & 0x3333u, T[2], T[3], 0x0040u),
+                                quintal_reg((hi >> 16) & 0x3333u, T[6], T[7], 0x0040u),
+                                quintal_reg((lo >> 18) & 0x3333u, T[2], T[3], 0x0051u),
+                                quintal_reg((hi >> 18) & 0x3333u, T[6], T[7], 0x0051u)};
         mma_chunk(c0 + u, A0, A1);
       }
     }
@@ -250,7 +321,7 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
                  torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
                  torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
                  c10::optional<torch::Tensor> miss_count, c10::optional<torch::Tensor> pool8, int64_t codes_off8,
-                 int64_t scale_off8, c10::optional<torch::Tensor> slot_table8) {
+                 int64_t scale_off8, c10::optional<torch::Tensor> slot_table8, bool quintal) {
   TORCH_CHECK(K % 64 == 0 && N % 16 == 0, "moe_w2_gemv: N % 16, K % 64");
   TORCH_CHECK(a.stride(1) == 1 && a.size(1) == K, "moe_w2_gemv: A [rows, K] inner-contiguous");
   TORCH_CHECK(sa.is_contiguous() && sa.size(1) == K / 64, "moe_w2_gemv: sA [rows, K/64]");
@@ -268,17 +339,21 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
   p.N = N; p.K = K;
   p.miss_count = miss_count.has_value() && miss_count->defined() ? miss_count->data_ptr<int>() : nullptr;
   p.pool8 = nullptr; p.slot_table8 = nullptr; p.slot_bytes8 = p.codes_off8 = p.scale_off8 = 0;
+  p.quintal = 0;
   if (pool8.has_value() && pool8->defined()) {
     TORCH_CHECK(slot_table8.has_value() && pool8->dim() == 2 && pool8->stride(0) % 16 == 0 && codes_off8 % 16 == 0 &&
                 scale_off8 % 16 == 0, "moe_w2_gemv: delta pool [slots, bytes] with a slot table, 16-byte aligned");
     p.pool8 = (const uint8_t*)pool8->data_ptr(); p.slot_bytes8 = pool8->stride(0);
     p.codes_off8 = codes_off8; p.scale_off8 = scale_off8; p.slot_table8 = slot_table8->data_ptr<int>();
+    p.quintal = quintal ? 1 : 0;
+    TORCH_CHECK(!quintal || codes_off8 % 8 == 0, "moe_w2_gemv: quintal plane offset");
   }
   const int max_pairs = pairs.size(0);
   const int wpc = 4;
   dim3 grid((N / 16 + wpc - 1) / wpc, max_pairs);
   auto stream = at::cuda::getCurrentCUDAStream();
-  const size_t smem = (size_t)wpc * 16 * (K / 32);
+  // scale stage per warp; split FP4 adds a 640-entry u16 digit table per warp
+  const size_t smem = (size_t)wpc * 16 * (K / 32) + (p.quintal ? (size_t)wpc * 640 * 2 : 0);
   TORCH_CHECK(smem <= 48 * 1024, "moe_w2_gemv: K too large for the shared scale stage");
   switch (rows_per_pair) {
     case 8: launch_k(moe_w2_gemv_kernel<1>, grid, wpc * 32, smem, stream, p); break;

@@ -673,3 +673,71 @@ def test_moe_gemv_delta_tier(C):
                 c13, s13, _, _ = lay.split(pool[e])
                 W = pl.dequant_plane(c13, s13, 2 * I, H).double()
             assert rel(out[po[t * k + j]].cpu(), A[t] @ W.t()) < 1e-4, (t, j, e)
+
+
+def test_moe_gemv_split_fp4_delta(C):
+    """Split FP4 (quintal) delta slots: the GEMV rebuilds the exact MXFP4 values from the
+    2-bit base codes + refinement digits (base scales); other experts read the 2-bit base;
+    an expert whose base slot is missing is a miss (zero rows), never a refinement alone."""
+    from vllm_moet_b200.residency.delta import split_layout, pack_split_slot, dequant_split_slot
+    from vllm_moet_b200.models.weights import ExpertLayout, quantize_experts_cpu
+    from vllm_moet_b200.formats import planes as pl
+    g = torch.Generator().manual_seed(7)
+    E, H, I, T, k, MB = 6, 256, 128, 3, 2, 8
+    w13 = torch.randn(E, 2 * I, H, generator=g) * 0.05
+    w2 = torch.randn(E, H, I, generator=g) * 0.05
+    lay = ExpertLayout(H=H, I=I)
+    pool = torch.empty(E, lay.slot_bytes, dtype=torch.uint8)
+    rows = []
+    for e in range(E):
+        n13, n2 = quantize_experts_cpu(w13[e:e + 1], w2[e:e + 1], lay, pool[e:e + 1], want_nibbles=True)
+        rows.append(pack_split_slot(n13, n2))
+    sbq, o13, _, o2, _ = split_layout(H, I)
+    pool8 = torch.zeros(3, sbq, dtype=torch.uint8)
+    table8 = torch.full((E,), -1, dtype=torch.int32)
+    for slot, e in enumerate((1, 4, 5)):
+        pool8[slot], table8[e] = rows[e], slot
+    base_table = torch.arange(E, dtype=torch.int32)
+    base_table[5] = -1                 # refinement present, base absent -> miss
+    ids = torch.tensor([[1, 2], [4, 1], [0, 5]], dtype=torch.int32)
+    R = T * k
+    P = R // MB + min(E, R)
+    rank = torch.empty(R, dtype=torch.int32, device=DEV); stok = torch.empty(R, dtype=torch.int32, device=DEV)
+    posof = torch.empty(R, dtype=torch.int32, device=DEV); pairs = torch.empty(P, 4, dtype=torch.int32, device=DEV)
+    npairs = torch.empty(1, dtype=torch.int32, device=DEV); st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    C.build_pairs(ids.to(DEV), E, MB, rank, stok, posof, pairs, npairs, st)
+    A = {}
+    outs = {}
+    for name, (N, K, oc, osc, oq) in {"w13": (2 * I, H, lay.off_codes13, lay.off_sc13, o13),
+                                      "w2": (H, I, lay.off_codes2, lay.off_sc2, o2)}.items():
+        x = torch.randn(T if name == "w13" else R, K, generator=g)
+        q, s = fp8.quant_act_fp8(x)
+        qw = fp8.to_w2_layout(q.view(torch.uint8)).to(DEV)
+        out = torch.full((R, N), float("nan"), device=DEV)
+        miss = torch.zeros(1, dtype=torch.int32, device=DEV)
+        C.moe_w2_gemv(qw, s.to(DEV), stok if name == "w13" else None, pairs, npairs, pool.to(DEV), oc, osc,
+                      base_table.to(DEV), out, N, K, MB, miss, pool8=pool8.to(DEV), codes_off8=oq, scale_off8=0,
+                      slot_table8=table8.to(DEV), quintal=True)
+        torch.cuda.synchronize()
+        A[name] = fp8.dequant_act_fp8(q, s).double()
+        outs[name] = (out.cpu(), int(miss))
+    po = posof.cpu().long()
+    for name in ("w13", "w2"):
+        out, miss = outs[name]
+        assert miss >= 1
+        for t in range(T):
+            for j in range(k):
+                e, r = int(ids[t, j]), int(po[t * k + j])
+                arow = A[name][t] if name == "w13" else A[name][r]
+                if e == 5:
+                    assert (out[r] == 0).all(), "a refinement without its base must not be served"
+                    continue
+                c13, s13, c2, s2 = lay.split(pool[e])
+                if int(table8[e]) >= 0:
+                    W = dequant_split_slot(rows[e], pl.unpack_codes(c13, 2 * I, H), pl.unpack_scales(s13, 2 * I, H),
+                                           pl.unpack_codes(c2, H, I), pl.unpack_scales(s2, H, I), H, I)
+                    W = (W[0] if name == "w13" else W[1]).double()
+                else:
+                    W = (pl.dequant_plane(c13, s13, 2 * I, H) if name == "w13"
+                         else pl.dequant_plane(c2, s2, H, I)).double()
+                assert rel(out[r], arow @ W.t()) < 1e-4, (name, t, j, e)

@@ -282,3 +282,72 @@ def test_pp_gate_barrier_consensus_and_fail_closed():
     assert all(o for o, _ in res) and all(c for _, c in res)     # every stage promoted and replays
     res = run_ranks(_pp_gate, 3, 1)
     assert not any(o for o, _ in res)                             # one failure -> nobody replays
+
+
+def test_split_fp4_slot_roundtrip_and_register_decode():
+    """Split-FP4 rows rebuild the exact MXFP4 values from the base codes + scales, and
+    the device decode (restated per lane) yields the direct-8 registers of those values."""
+    from vllm_moet_b200.formats import codebook, planes
+    from vllm_moet_b200.residency.delta import dequant_split_slot, pack_split_slot, split_layout
+    g = torch.Generator().manual_seed(3)
+    H, I = 128, 64
+    nib13 = torch.randint(0, 16, (2 * I, H), generator=g, dtype=torch.uint8)
+    nib2 = torch.randint(0, 16, (H, I), generator=g, dtype=torch.uint8)
+    sc13 = torch.randint(115, 135, (2 * I, H // 32), generator=g, dtype=torch.uint8)
+    sc2 = torch.randint(115, 135, (H, I // 32), generator=g, dtype=torch.uint8)
+    row = pack_split_slot(nib13, nib2)
+    assert row.numel() == split_layout(H, I)[0] == (2 * I * H + H * I) * 5 // 16
+    w13, w2 = dequant_split_slot(row, codebook.nibbles_to_codes(nib13), sc13, codebook.nibbles_to_codes(nib2), sc2,
+                                 H, I)
+    for w, nib, sc in ((w13, nib13, sc13), (w2, nib2, sc2)):
+        N, K = nib.shape
+        want = codebook.E2M1_VALUES[nib.long()].float().view(N, K // 32, 32) * torch.exp2(sc.float() - 127)[..., None]
+        assert torch.equal(w, want.view(N, K))
+    # per-lane device decode == direct-8 registers, every lane of every block of w13
+    N, K = nib13.shape
+    cp = planes.pack_codes(codebook.nibbles_to_codes(nib13))
+    qp = planes.pack_quintal(nib13)
+    d8 = planes.pack_direct8(planes.e2m1_to_e4m3_bytes(nib13))
+    for blk in range((N // 16) * (K // 64)):
+        for lane in range(32):
+            cb = bytes(cp[blk * 256 + lane * 8: blk * 256 + lane * 8 + 8].tolist())
+            rec = bytes(qp[blk * 320 + lane * 8: blk * 320 + lane * 8 + 8].tolist()) + \
+                bytes(qp[blk * 320 + 256 + lane * 2: blk * 320 + 258 + lane * 2].tolist())
+            A0, A1 = planes.quintal_lane_registers(cb, rec)
+            got = b"".join(x.to_bytes(4, "little") for x in A0 + A1)
+            assert list(got) == d8[blk * 1024 + lane * 32: blk * 1024 + lane * 32 + 32].tolist(), (blk, lane)
+    for w in range(625):                      # the multiply-shift divide by 5 gives the base-5 digits
+        t = planes.quintal_digit_word(w)
+        d = [t & 0xF, (t >> 8) & 0xF, (t >> 4) & 0xF, (t >> 12) & 0xF]
+        assert sum(di * 5 ** i for i, di in enumerate(d)) == w and max(d) < 5
+
+
+def test_split_delta_coupling_protects_the_base(tmp_path):
+    """A split-FP4 promotion makes the base resident first, and the base cache
+    never evicts an expert that has a delta slot."""
+    from vllm_moet_b200.residency.delta import DeltaTier, split_layout
+    H = I = 64
+    sbq = split_layout(H, I)[0]
+    base = _cache(tmp_path, slots=4)
+    rows = [torch.randint(0, 256, (E, sbq), dtype=torch.uint8) for _ in range(L)]
+    delta = DeltaTier(rows, H, I, 3, device="cpu", policy="need", split=True)
+    try:
+        delta.couple(base)
+        assert delta.promote([(0, 1), (1, 2)]) == 2
+        assert base.resident(0, 1) and base.resident(1, 2) and delta.resident(0, 1)
+        base.step_end(), delta.step_end()
+        base.promote([(2, 0), (2, 1)])          # fills the base pool
+        base.step_end()
+        base.promote([(2, 2)])                  # must evict (2, 0) or (2, 1), never a coupled expert
+        assert base.resident(0, 1) and base.resident(1, 2) and base.resident(2, 2)
+        base.step_end()
+        base.note_routed(2, [2])
+        before = base.mirror.clone()
+        with pytest.raises(FetchError):         # one unprotected, unpinned slot for two experts
+            base.promote([(2, 3), (2, 4)])
+        assert torch.equal(base.mirror, before)     # all or nothing: the victim taken first is restored
+        for li in range(L):
+            for e in range(E):
+                assert int(base.slot_table[li, e]) == int(base.mirror[li, e])
+    finally:
+        delta.close()

@@ -79,3 +79,51 @@ def test_delta_tier_and_gate(resident_tokens):
         row = lg[-1]
         assert float(row[tok]) >= float(row.max()) - 0.5 * (float(row.std()) + 1e-6), (tok, int(row.argmax()))
         seq.append(tok)
+
+
+def test_split_fp4_delta_and_gate(resident_tokens, monkeypatch):
+    """Split FP4 delta slots (quintal refinement over the resident 2-bit base): with the
+    gate quiet the tokens equal the base engine; with the gate always firing every decode
+    step replays on FP4 experts rebuilt from base codes + refinement digits, and the tokens
+    track an oracle whose experts are those exact MXFP4 values."""
+    from vllm_moet_b200.formats import planes as pl
+    from vllm_moet_b200.models import reference
+    from vllm_moet_b200.residency import moe_layers
+    from vllm_moet_b200.residency.delta import dequant_split_slot
+    monkeypatch.setenv("VLLM_MOE_W2_DELTA_SPLIT", "1")
+    quiet = LLM(_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=512, max_num_seqs=2,
+                delta_slots=48, gate=True)
+    assert quiet.delta.split
+    quiet.gate.tau = -1.0
+    out = [o.outputs[0].token_ids for o in quiet.generate(_prompts(), SamplingParams(max_tokens=12, ignore_eos=True))]
+    assert out == resident_tokens
+    quiet.shutdown()
+    del quiet
+    torch.cuda.empty_cache()
+    loud = LLM(_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=512, max_num_seqs=2,
+               delta_slots=48, gate=True)
+    loud.gate.tau = 2.0
+    p = _prompts()[0]
+    toks = loud.generate([p], SamplingParams(max_tokens=6, ignore_eos=True))[0].outputs[0].token_ids
+    assert loud.delta.stats["gate_replays"] > 0 and loud.delta.stats["fetched_rows"] > 0
+    loud.runner.check_status("split fp4")
+    lay = moe_layers(loud.mw)[0].experts.layout
+    H, I = lay.H, lay.I
+    for li, lw in enumerate(moe_layers(loud.mw)):
+        rows = loud.delta.store.layers[li]
+        w13s, w2s = [], []
+        for e in range(rows.shape[0]):
+            c13, s13, c2, s2 = lay.split(lw.experts.pool[e].cpu())
+            a, b = dequant_split_slot(rows[e].cpu(), pl.unpack_codes(c13, 2 * I, H), pl.unpack_scales(s13, 2 * I, H),
+                                      pl.unpack_codes(c2, H, I), pl.unpack_scales(s2, H, I), H, I)
+            w13s.append(a), w2s.append(b)
+        lw.experts.dense_w13 = torch.stack(w13s).cuda()
+        lw.experts.dense_w2 = torch.stack(w2s).cuda()
+    cs = reference.rope_cos_sin(loud.cfg, 256, "cuda")
+    seq = list(p) + [toks[0]]
+    for tok in toks[1:]:
+        lg, _ = reference.forward(loud.mw, torch.tensor(seq, device="cuda"), torch.arange(len(seq), device="cuda"), cs)
+        row = lg[-1]
+        assert float(row[tok]) >= float(row.max()) - 0.5 * (float(row.std()) + 1e-6), (tok, int(row.argmax()))
+        seq.append(tok)
+    loud.shutdown()

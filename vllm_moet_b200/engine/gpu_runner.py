@@ -560,8 +560,9 @@ class NativeRunner:
         if self.delta is not None and mli is not None:    # FP4 delta slots first, 2-bit base otherwise
             o13, os13, o2, os2 = self.delta.offsets
             t8 = self.delta.slot_table[mli]
-            d13 = dict(pool8=self.delta.pool, codes_off8=o13, scale_off8=os13, slot_table8=t8)
-            d2 = dict(pool8=self.delta.pool, codes_off8=o2, scale_off8=os2, slot_table8=t8)
+            q = bool(getattr(self.delta, "split", False))
+            d13 = dict(pool8=self.delta.pool, codes_off8=o13, scale_off8=os13, slot_table8=t8, quintal=q)
+            d2 = dict(pool8=self.delta.pool, codes_off8=o2, scale_off8=os2, slot_table8=t8, quintal=q)
         c13 = self.ws.get("c13", (R, 2 * I), torch.float32)
         C.moe_w2_gemv(h2q, h2s, stok, pairs, npairs, ex.pool, L.off_codes13, L.off_sc13, ex.slot_table, c13,
                       2 * I, H, MB, self.miss, **d13)

@@ -80,7 +80,8 @@ class LLM:
         self.mw = weights if weights is not None else random_weights(
             cfg, self.device, seed=seed, tp_rank=tp_rank, tp_size=tensor_parallel_size,
             with_mtp=num_speculative_tokens > 0, pp_rank=pp_rank, pp_size=pipeline_parallel_size,
-            with_delta=bool(delta_slots) and self.device.type == "cuda", expert_parallel=expert_parallel,
+            with_delta=(("split" if self.ecfg.moet.delta_split else True) if delta_slots and self.device.type == "cuda"
+                        else False), expert_parallel=expert_parallel,
             expert_source=self.expert_source)
         if self.expert_source is not None:
             self.expert_source.flush()
@@ -166,7 +167,9 @@ class LLM:
             raise ValueError("delta tier needs weights built with delta rows")
         lay = layers[0].experts.layout
         self.delta = DeltaTier(rows, lay.H, lay.I, slots, device=self.device, policy=m.delta_policy,
-                               decay=m.delta_decay)
+                               decay=m.delta_decay, split=m.delta_split)
+        if getattr(self, "cache", None) is not None:
+            self.delta.couple(self.cache)
         for lw in layers:
             lw.experts.delta_rows = None
         self.runner.attach_delta_tier(self.delta)

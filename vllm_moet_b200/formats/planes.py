@@ -232,3 +232,63 @@ def dequant_direct8(plane: torch.Tensor, scale_plane: torch.Tensor, N: int, K: i
     b = unpack_direct8(plane, N, K).view(torch.float8_e4m3fn).float()
     s = torch.exp2(unpack_scales(scale_plane, N, K).float() - 127.0)
     return (b.view(N, K // 32, 32) * s[..., None]).view(N, K)
+
+
+# ---- split FP4 (w4q) device decode, restated on the host ------------------------
+#
+# The expert GEMV's quintal mode builds each lane's MMA A-fragment registers from
+# the lane's 8 base-code bytes and its 10-byte quintal record.  This is the same
+# integer arithmetic, one lane at a time, so the device decode has an exact oracle:
+# the registers must equal the lane's bytes of the direct-8 container of the
+# reconstructed e2m1 values.
+
+E4M3_LUT_WORD = 0x4838B8C8                   # code -> e4m3 level {-4, -1, +1, +4}
+E2M1_MAG_E4M3 = (0x3C383000, 0x4C484440)     # magnitude index 0..7 -> e4m3 byte {0, .5, 1, 1.5, 2, 3, 4, 6}
+
+
+def prmt(a: int, b: int, sel: int) -> int:
+    """PTX prmt (default mode) on Python ints: output byte i = byte (sel nibble i & 7) of {b:a}."""
+    pool = (a & 0xFFFFFFFF) | ((b & 0xFFFFFFFF) << 32)
+    out = 0
+    for i in range(4):
+        s = (sel >> (4 * i)) & 0xF
+        byte = (pool >> (8 * (s & 7))) & 0xFF
+        if s & 8:                                 # sign-replicate mode (not used by the decode)
+            byte = 0xFF if byte & 0x80 else 0x00
+        out |= byte << (8 * i)
+    return out
+
+
+def quintal_digit_word(w: int) -> int:
+    """10-bit quintal word -> (d0 | d2 << 4) | (d1 | d3 << 4) << 8, digits by the
+    multiply-shift divide by 5 ((x * 0x334) >> 12, exact below 1024)."""
+    q1 = (w * 0x334) >> 12
+    d0 = w - 5 * q1
+    q2 = (q1 * 0x334) >> 12
+    d1 = q1 - 5 * q2
+    q3 = (q2 * 0x334) >> 12
+    d2 = q2 - 5 * q3
+    d3 = q3
+    return (d0 | (d2 << 4)) | ((d1 | (d3 << 4)) << 8)
+
+
+def quintal_lane_registers(code_bytes: bytes, rec: bytes):
+    """One lane: 8 base-code bytes + 10-byte quintal record -> (A0[4], A1[4]) e4m3 words."""
+    lo = int.from_bytes(code_bytes[:4], "little")
+    hi = int.from_bytes(code_bytes[4:8], "little")
+    r = int.from_bytes(rec[:8], "little") | (int.from_bytes(rec[8:10], "little") << 64)
+    T = [quintal_digit_word((r >> (10 * b)) & 0x3FF) for b in range(8)]
+
+    def reg(c_sel: int, ga: int, gb: int, odd: bool) -> int:
+        base = prmt(E4M3_LUT_WORD, E4M3_LUT_WORD, c_sel)
+        dsel = prmt(T[ga], T[gb], 0x0051 if odd else 0x0040) & 0xFFFF
+        big = ~(c_sel ^ (c_sel >> 1)) & 0x1111          # code 0 or 3: the {3, 4, 6} class
+        mag = prmt(E2M1_MAG_E4M3[0], E2M1_MAG_E4M3[1], dsel + 5 * big)
+        return mag | (base & 0x80808080)
+
+    m = 0x3333
+    A0 = [reg(lo & m, 0, 1, False), reg(hi & m, 4, 5, False), reg((lo >> 2) & m, 0, 1, True),
+          reg((hi >> 2) & m, 4, 5, True)]
+    A1 = [reg((lo >> 16) & m, 2, 3, False), reg((hi >> 16) & m, 6, 7, False), reg((lo >> 18) & m, 2, 3, True),
+          reg((hi >> 18) & m, 6, 7, True)]
+    return A0, A1

@@ -252,17 +252,23 @@ def quantize_experts_gpu(w13: torch.Tensor, w2: torch.Tensor, layout: ExpertLayo
 
 
 def quantize_experts_cpu(w13: torch.Tensor, w2: torch.Tensor, layout: ExpertLayout, out_pool: torch.Tensor,
-                         zero_mode: str = "auto"):
-    """Golden torch pipeline (NVFP4 -> f64 -> 2-bit) for CPU / tests."""
+                         zero_mode: str = "auto", want_nibbles: bool = False):
+    """Golden torch pipeline (NVFP4 -> f64 -> 2-bit) for CPU / tests.  With
+    want_nibbles, also -> the e2m1 nibbles (w13, w2) of the last expert, the exact
+    values the codes were taken from (the split-FP4 refinement source)."""
+    nibs = None
     for e in range(w13.shape[0]):
+        nibs = []
         for (mat, off_c, off_s) in ((w13[e], layout.off_codes13, layout.off_sc13),
                                     (w2[e], layout.off_codes2, layout.off_sc2)):
             N, K = mat.shape
             ts = float(mat.abs().max()) / (6.0 * 448.0) or 1.0
             packed, sf, t2 = codebook.f32_to_nvfp4(mat.float().cpu(), ts)
-            codes, sc, _ = codebook.nvfp4_to_codes_scales(packed, sf, t2, mode=zero_mode)
+            codes, sc, nib = codebook.nvfp4_to_codes_scales(packed, sf, t2, mode=zero_mode, want_nibbles=want_nibbles)
             out_pool[e, off_c:off_c + N * K // 4] = planes.pack_codes(codes).to(out_pool.device)
             out_pool[e, off_s:off_s + N * K // 32] = planes.pack_scales(sc).to(out_pool.device)
+            nibs.append(nib)
+    return tuple(nibs) if want_nibbles else None
 
 
 def _pad_to(n: int, m: int) -> int:
@@ -402,11 +408,17 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
         w13 = shard13(rng.normal((n, 2 * Ifull, H)))[a - e0:b - e0]
         w2 = shard2(rng.normal((n, H, Ifull)))[a - e0:b - e0]
         n, e0 = b - a, a - e_lo
-        if torch.device(dev).type == "cuda":
+        if with_delta == "split":        # base + refinement from one quantiser run (host side)
+            from ..residency.delta import pack_split_slot
+            for i in range(n):
+                nibs = quantize_experts_cpu(w13[i:i + 1], w2[i:i + 1], layout, pool[e0 + i:e0 + i + 1],
+                                            want_nibbles=True)
+                delta_rows.append(pack_split_slot(*nibs))
+        elif torch.device(dev).type == "cuda":
             quantize_experts_gpu(w13, w2, layout, pool[e0:e0 + n])
         else:
             quantize_experts_cpu(w13, w2, layout, pool[e0:e0 + n])
-        if delta_rows is not None:       # FP4 delta-tier rows of the same experts (host side)
+        if delta_rows is not None and with_delta != "split":   # FP4 delta-tier rows of the same experts
             from ..residency.delta import pack_delta_slot
             delta_rows += [pack_delta_slot(w13[i], w2[i]) for i in range(n)]
         del w13, w2

@@ -13,6 +13,15 @@ P:8063-8383, P:10290-10350).  Policies:
   routed experts, then replay the step);
 * ``lru``  -- like ``need``, evicting the least recently used slot.
 
+Split FP4 (``split=True``, the reference's ``DELTA_SPLIT`` / w4q path, patch
+P:8243-8247, P:8811-8827, P:10031-10055): a delta slot holds only the quintal
+refinement planes ``[q13 (2I*H*5/16) | q2 (H*I*5/16)]``, read against the
+resident 2-bit base slot (its codes pick each element's magnitude class and
+sign, its UE8M0 scales are the MXFP4 scales), so the GEMV rebuilds the exact
+e2m1 values from 2 + 2.5 bits per weight.  The pair is served from the delta
+slot only while the base slot is resident, and a base cache never evicts an
+expert that has a delta slot (:meth:`DeltaTier.couple`).
+
 The pool / table / host-store machinery is :class:`.tier.ExpertCache`.
 """
 from __future__ import annotations
@@ -35,6 +44,32 @@ def delta_layout(H: int, I: int):
     return c13 + s13 + c2 + s2, 0, c13, c13 + s13, c13 + s13 + c2
 
 
+def split_layout(H: int, I: int):
+    """-> (slot_bytes, q13, 0, q2, 0): split-FP4 slot offsets (no scale planes of its own)."""
+    q13 = planes.quintal_plane_bytes(2 * I, H)
+    q2 = planes.quintal_plane_bytes(H, I)
+    return q13 + q2, 0, 0, q13, 0
+
+
+def pack_split_slot(nib13: torch.Tensor, nib2: torch.Tensor) -> torch.Tensor:
+    """e2m1 nibbles of w13 [2I, H] and w2 [H, I] (the nibbles the base codes were
+    derived from) -> one split-FP4 delta slot row (u8)."""
+    return torch.cat([planes.pack_quintal(nib13.cpu()), planes.pack_quintal(nib2.cpu())])
+
+
+def dequant_split_slot(row: torch.Tensor, codes13: torch.Tensor, sc13: torch.Tensor, codes2: torch.Tensor,
+                       sc2: torch.Tensor, H: int, I: int):
+    """Split slot + the base's codes / UE8M0 scales ([N, K] / [N, K/32]) -> float (w13, w2)."""
+    from ..formats.codebook import E2M1_VALUES
+    sb, _, _, o2, _ = split_layout(H, I)
+    out = []
+    for plane, codes, sc, (N, K) in ((row[:o2], codes13, sc13, (2 * I, H)), (row[o2:sb], codes2, sc2, (H, I))):
+        nib = planes.quintal_reconstruct(codes, planes.unpack_quintal_digits(plane, N, K))
+        v = E2M1_VALUES[nib.long()].float()
+        out.append((v.view(N, K // 32, 32) * torch.exp2(sc.float() - 127.0)[..., None]).view(N, K))
+    return tuple(out)
+
+
 def pack_delta_slot(w13: torch.Tensor, w2: torch.Tensor) -> torch.Tensor:
     """float expert matrices w13 [2I, H], w2 [H, I] -> one delta slot row (u8)."""
     parts = []
@@ -54,10 +89,12 @@ def dequant_delta_slot(row: torch.Tensor, H: int, I: int):
 
 class DeltaTier(ExpertCache):
     def __init__(self, rows_per_layer: List[torch.Tensor], H: int, I: int, n_slots: int, device="cuda",
-                 policy: str = "freq", decay: float = 0.98):
+                 policy: str = "freq", decay: float = 0.98, split: bool = False):
         L = len(rows_per_layer)
         E = rows_per_layer[0].shape[0]
-        self.layout = delta_layout(H, I)
+        self.split = split
+        self.base = None
+        self.layout = split_layout(H, I) if split else delta_layout(H, I)
         sb = self.layout[0]
         store = make_store("pinned", L, E, sb)
         for li, r in enumerate(rows_per_layer):
@@ -65,6 +102,19 @@ class DeltaTier(ExpertCache):
         super().__init__(store, L, E, sb, n_slots, device=device, policy="lru" if policy == "lru" else "freq",
                          decay=decay, manager=True)
         self.delta_policy = policy
+
+    def couple(self, base_cache) -> None:
+        """Split FP4 over a base expert cache: promotions make the base resident
+        first, and the base never evicts an expert that has a delta slot."""
+        if not self.split:
+            return
+        self.base = base_cache
+        base_cache.protect = lambda li, e: self.resident(li, e)
+
+    def promote(self, pairs, stream=None, sync: bool = True) -> int:
+        if self.base is not None:
+            self.base.promote(pairs, stream=stream, sync=sync)   # a refinement is read against its base
+        return super().promote(pairs, stream=stream, sync=sync)
 
     @property
     def offsets(self):

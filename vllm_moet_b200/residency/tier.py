@@ -59,6 +59,7 @@ class ExpertCache:
         self.last_use = [0.0] * self.n_slots
         self.freq = torch.zeros(n_layers, E, dtype=torch.float32)
         self.pinned: set = set()
+        self.protect = None            # (li, e) -> True: never evict (split-FP4 delta slots read this base)
         self.free = list(range(self.n_slots - 1, -1, -1))
         self.step = 0
         self.lock = threading.RLock()
@@ -107,6 +108,8 @@ class ExpertCache:
             if s in self.pinned or s in protect or self.owner[s] is None:
                 continue
             li, e = self.owner[s]
+            if self.protect is not None and self.protect(li, e):
+                continue
             key = self.last_use[s] if self.policy == "lru" else (float(self.freq[li, e]), self.last_use[s])
             if best_key is None or key < best_key:
                 best, best_key = s, key
@@ -115,18 +118,31 @@ class ExpertCache:
         return best
 
     def _take_slots(self, n: int, protect: set, evicted: list) -> List[int]:
-        out = []
-        for _ in range(n):
-            if self.free:
-                out.append(self.free.pop())
-            else:
-                s = self._victim(protect | set(out))
-                li, e = self.owner[s]
-                self.mirror[li, e] = -1
-                self.owner[s] = None
-                evicted.append((li, e))
-                self.stats["evictions"] += 1
-                out.append(s)
+        """n slots (free first, then victims).  All or nothing: if a victim cannot be
+        found, every slot taken so far goes back to its owner or the free list."""
+        out, from_free = [], []
+        try:
+            for _ in range(n):
+                if self.free:
+                    s = self.free.pop()
+                    from_free.append(s)
+                    out.append(s)
+                else:
+                    s = self._victim(protect | set(out))
+                    li, e = self.owner[s]
+                    self.mirror[li, e] = -1
+                    self.owner[s] = None
+                    evicted.append((li, e, s))
+                    out.append(s)
+        except FetchError:
+            for li, e, s in evicted:
+                self.mirror[li, e] = s
+                self.owner[s] = (li, e)
+            self.free.extend(reversed(from_free))
+            evicted.clear()
+            raise
+        self.stats["evictions"] += len(evicted)
+        evicted[:] = [(li, e) for li, e, _ in evicted]
         return out
 
     # ------------------------------------------------------------------ fetch
