@@ -385,21 +385,22 @@ __global__ void mla_combine_kernel(const float* __restrict__ o_part, const float
 // (bf16-rounded, kept in shared memory), applies W_uv[h] (128 x 512, e4m3 with
 // UE8M0 128x128 block scales) and writes ov[t, h*128 + j] as e4m3 with UE8M0
 // per-64 scales -- the input of the o projection.
-constexpr int kVD = 128, kTC = 16;   // value head dim, tokens per smem chunk
+constexpr int kTC = 16;   // tokens per smem chunk
 __global__ void __launch_bounds__(256) mla_combine_uv_kernel(const float* __restrict__ o_part,
                                                              const float* __restrict__ ml_part, int S, int T, int Hh,
                                                              const uint8_t* __restrict__ wuv,
                                                              const uint8_t* __restrict__ swuv,
-                                                             uint8_t* __restrict__ q, uint8_t* __restrict__ qs) {
+                                                             uint8_t* __restrict__ q, uint8_t* __restrict__ qs,
+                                                             int VD) {
   __shared__ __align__(16) float olat[kTC][kLat];
-  __shared__ float ov[kTC][kVD / 2];
+  __shared__ float ov[kTC][64];
   __shared__ float wgt[kTC][32];
   __shared__ int nact[kTC];
   const int h = blockIdx.x, TH = T * Hh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint8_t* W = wuv + (size_t)h * kVD * kLat;
-  const uint8_t* SW = swuv + (size_t)h * (kLat / 128);
-  // CTA (head h, half hv) computes output rows [64 hv, 64 hv + 64) -- exactly one quantisation group;
+  const uint8_t* W = wuv + (size_t)h * VD * kLat;
+  const uint8_t* SW = swuv + (size_t)h * (VD / 128) * (kLat / 128);   // [VD/128, 4] block scales of this head
+  // CTA (head h, group hv) computes output rows [64 hv, 64 hv + 64) -- exactly one quantisation group;
   // thread (row j, quarter qk) owns W[j][128*qk .. +128) -- one scale block; immutable, so it is
   // loaded before the dependency wait
   const int hv = blockIdx.y;
@@ -408,7 +409,7 @@ __global__ void __launch_bounds__(256) mla_combine_uv_kernel(const float* __rest
 #pragma unroll
   for (int u = 0; u < 8; u++)
     wrow[u] = __ldg(reinterpret_cast<const uint4*>(W + (size_t)j * kLat + qk * 128) + u);
-  const float wsc = ue8m0_to_float(__ldg(SW + qk));
+  const float wsc = ue8m0_to_float(__ldg(SW + (j >> 7) * (kLat / 128) + qk));
   pdl_entry();
   const int tbeg = blockIdx.z * kTC, tend = min(T, tbeg + kTC);
   for (int t0 = tbeg; t0 < tend; t0 += kTC) {
@@ -478,11 +479,11 @@ __global__ void __launch_bounds__(256) mla_combine_uv_kernel(const float* __rest
       const float amax = warp_max(fmaxf(fabsf(a), fabsf(b)));
       const uint32_t e = ue8m0_for_amax(amax);
       const float inv = (e >= 1 && e <= 253) ? __uint_as_float((254u - e) << 23) : 0.f;
-      const size_t col = (size_t)h * kVD + g0;
-      uint8_t* dq = q + (size_t)(t0 + tt) * Hh * kVD + col + 2 * lane;
+      const size_t col = (size_t)h * VD + g0;
+      uint8_t* dq = q + (size_t)(t0 + tt) * Hh * VD + col + 2 * lane;
       dq[0] = f32_to_e4m3(a * inv);
       dq[1] = f32_to_e4m3(b * inv);
-      if (lane == 0) qs[(size_t)(t0 + tt) * (Hh * kVD / 64) + col / 64] = (uint8_t)e;
+      if (lane == 0) qs[(size_t)(t0 + tt) * (Hh * VD / 64) + col / 64] = (uint8_t)e;
     }
     __syncthreads();
   }
@@ -497,15 +498,17 @@ void mla_combine_uv(torch::Tensor o_part, torch::Tensor ml_part, torch::Tensor w
   const int S = o_part.size(0), T = o_part.size(1), Hh = o_part.size(2);
   TORCH_CHECK(o_part.size(3) == kLat && S <= 32 && o_part.is_contiguous() && ml_part.is_contiguous(),
               "mla_combine_uv: o_part [S<=32, T, Hh, 512] contiguous");
-  TORCH_CHECK(wuv.dim() == 3 && wuv.size(0) == Hh && wuv.size(1) == kVD && wuv.size(2) == kLat && wuv.is_contiguous(),
-              "mla_combine_uv: W_uv [Hh, 128, 512]");
-  TORCH_CHECK(swuv.numel() == (int64_t)Hh * (kLat / 128) && swuv.is_contiguous(), "mla_combine_uv: W_uv scales [Hh, 1, 4]");
-  TORCH_CHECK(q.is_contiguous() && q.size(-1) * (q.dim() == 3 ? q.size(1) : 1) == (int64_t)Hh * kVD, "mla_combine_uv: out");
+  const int VD = wuv.size(1);
+  TORCH_CHECK(wuv.dim() == 3 && wuv.size(0) == Hh && VD % 128 == 0 && VD <= 512 && wuv.size(2) == kLat &&
+              wuv.is_contiguous(), "mla_combine_uv: W_uv [Hh, VD (128 | 256 ...), 512]");
+  TORCH_CHECK(swuv.numel() == (int64_t)Hh * (VD / 128) * (kLat / 128) && swuv.is_contiguous(),
+              "mla_combine_uv: W_uv scales [Hh, VD/128, 4]");
+  TORCH_CHECK(q.is_contiguous() && q.size(-1) * (q.dim() == 3 ? q.size(1) : 1) == (int64_t)Hh * VD, "mla_combine_uv: out");
   if (T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  launch_k(mla_combine_uv_kernel, dim3(Hh, 2, (T + kTC - 1) / kTC), 256, 0, stream, o_part.data_ptr<float>(), ml_part.data_ptr<float>(), S, T, Hh,
+  launch_k(mla_combine_uv_kernel, dim3(Hh, VD / 64, (T + kTC - 1) / kTC), 256, 0, stream, o_part.data_ptr<float>(), ml_part.data_ptr<float>(), S, T, Hh,
            (const uint8_t*)wuv.data_ptr(), (const uint8_t*)swuv.data_ptr(), (uint8_t*)q.data_ptr(),
-           (uint8_t*)qs.data_ptr());
+           (uint8_t*)qs.data_ptr(), VD);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -1,5 +1,8 @@
-// MLA prefill attention (non-absorbed): per head, q = [q_nope | q_rope] (192),
-// k = [k_nope (from kv_b) | k_rope (shared by all heads)] (192), v (128).
+// MLA prefill attention (non-absorbed): per head, q = [q_nope | q_rope] (DN + 64),
+// k = [k_nope (from kv_b) | k_rope (shared by all heads)] (DN + 64), v (DV).
+// DN = 128 / DV = 128 (DeepSeek-V4 shape) or DN = 192 / DV = 256 (GLM-5.x shape).
+// A CTA accumulates 128 value columns; with DV = 256 two CTAs share a head (each
+// recomputes Q.K^T), which keeps the O accumulator at 64 registers per thread.
 // Causal within each sequence of a varlen batch (cu_seqlens).  Flash-attention
 // structure: a CTA owns 128 query rows of one head (8 warps x 16 rows), Q
 // fragments stay in registers, K/V tiles of 64 keys are double-buffered in
@@ -12,9 +15,8 @@
 
 namespace moet {
 
-constexpr int kD = 192, kDN = 128, kDV = 128;
+constexpr int kDV = 128;  // value columns per CTA
 constexpr int kBQ = 128, kBK = 64;
-constexpr int kKS = 200;  // K smem row (bf16)
 constexpr int kVS = 136;  // V smem row (bf16)
 
 MOET_DEVICE void cp_async16(void* dst, const void* src, bool pred) {
@@ -26,21 +28,26 @@ MOET_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
 template <int N> MOET_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
 
 struct PrefillArgs {
-  const __nv_bfloat16* q; long long q_tok_stride; int q_head_stride;     // [T, Hh, 192]
-  const __nv_bfloat16* kvb; long long kvb_tok_stride; int kvb_head_stride; // [T, Hh, 256] = k_nope | v
+  const __nv_bfloat16* q; long long q_tok_stride; int q_head_stride;     // [T, Hh, DN + 64]
+  const __nv_bfloat16* kvb; long long kvb_tok_stride; int kvb_head_stride; // [T, Hh, DN + DV] = k_nope | v
   const __nv_bfloat16* kr; long long kr_tok_stride;                      // [T, 64]
   const int* cu_seqlens; int nseq;
-  int Hh;
+  int Hh, DV;
   float scale_log2;
-  uint8_t* out_q; uint8_t* out_s; __nv_bfloat16* out_bf16;   // [T, Hh*128]
+  uint8_t* out_q; uint8_t* out_s; __nv_bfloat16* out_bf16;   // [T, Hh*DV]
 };
 
+template <int kDN>
 __global__ void __launch_bounds__(256, 1) mla_prefill_kernel(PrefillArgs p) {
+  constexpr int kD = kDN + 64;
+  constexpr int kKS = kD + 8;   // K / Q smem row (bf16): an odd number of 16-byte units
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);   // [2][64][200]
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);   // [2][64][kKS]
   __nv_bfloat16* Vs = Ks + 2 * kBK * kKS;                             // [2][64][136]
-  __nv_bfloat16* Qs = Vs + 2 * kBK * kVS;                             // [128][200]
-  const int qtile = blockIdx.x, h = blockIdx.y, sq = blockIdx.z;
+  __nv_bfloat16* Qs = Vs + 2 * kBK * kVS;                             // [128][kKS]
+  const int nvc = p.DV / kDV;
+  const int qtile = blockIdx.x, h = blockIdx.y / nvc, vc = blockIdx.y % nvc, sq = blockIdx.z;
+  const int vcol0 = vc * kDV;                                         // this CTA's value columns
   const int s0 = p.cu_seqlens[sq], n = p.cu_seqlens[sq + 1] - s0;
   const int q0 = qtile * kBQ;
   if (q0 >= n) return;
@@ -70,8 +77,8 @@ __global__ void __launch_bounds__(256, 1) mla_prefill_kernel(PrefillArgs p) {
       const int r = i / (kDV / 8), c = (i % (kDV / 8)) * 8;
       const int tok = k0 + r;
       const int tt = s0 + min(tok, n - 1);
-      cp_async16(vd + r * kVS + c, p.kvb + (size_t)tt * p.kvb_tok_stride + (size_t)h * p.kvb_head_stride + kDN + c,
-                 tok < n);
+      cp_async16(vd + r * kVS + c,
+                 p.kvb + (size_t)tt * p.kvb_tok_stride + (size_t)h * p.kvb_head_stride + kDN + vcol0 + c, tok < n);
     }
   };
   const int nkt = min((q0 + kBQ + kBK - 1) / kBK, (n + kBK - 1) / kBK);
@@ -175,7 +182,8 @@ __global__ void __launch_bounds__(256, 1) mla_prefill_kernel(PrefillArgs p) {
   }
   // epilogue
   const float inv0 = l_run[0] > 0.f ? 1.f / l_run[0] : 0.f, inv1 = l_run[1] > 0.f ? 1.f / l_run[1] : 0.f;
-  const int HD = p.Hh * kDV;
+  const int HD = p.Hh * p.DV;
+  const int ocol0 = h * p.DV + vcol0;
 #pragma unroll
   for (int hr = 0; hr < 2; hr++) {
     const int qr = hr ? qrow1 : qrow0;
@@ -191,7 +199,7 @@ __global__ void __launch_bounds__(256, 1) mla_prefill_kernel(PrefillArgs p) {
     if (p.out_bf16 && valid) {
 #pragma unroll
       for (int i = 0; i < kDV / 8; i++)
-        *reinterpret_cast<__nv_bfloat162*>(p.out_bf16 + row * HD + h * kDV + i * 8 + 2 * t) =
+        *reinterpret_cast<__nv_bfloat162*>(p.out_bf16 + row * HD + ocol0 + i * 8 + 2 * t) =
             __floats2bfloat162_rn(v[i][0], v[i][1]);
     }
     if (p.out_q) {
@@ -208,9 +216,9 @@ __global__ void __launch_bounds__(256, 1) mla_prefill_kernel(PrefillArgs p) {
 #pragma unroll
           for (int i = gi * 8; i < gi * 8 + 8; i++) {
             const uint16_t b = (uint16_t)f32_to_e4m3(v[i][0] * invs) | ((uint16_t)f32_to_e4m3(v[i][1] * invs) << 8);
-            *reinterpret_cast<uint16_t*>(p.out_q + row * HD + h * kDV + i * 8 + 2 * t) = b;
+            *reinterpret_cast<uint16_t*>(p.out_q + row * HD + ocol0 + i * 8 + 2 * t) = b;
           }
-          if (t == 0) p.out_s[row * (HD / 64) + (h * kDV) / 64 + gi] = (uint8_t)e;
+          if (t == 0) p.out_s[row * (HD / 64) + ocol0 / 64 + gi] = (uint8_t)e;
         }
       }
     }
@@ -225,22 +233,28 @@ void mla_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kr, torch::Te
                  double scale, c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_s,
                  c10::optional<torch::Tensor> out_bf16) {
   const int Hh = q.size(1);
-  TORCH_CHECK(q.size(2) == kD && q.stride(2) == 1, "mla_prefill: q [T, Hh, 192]");
-  TORCH_CHECK(kvb.size(2) == kDN + kDV && kvb.stride(2) == 1, "mla_prefill: kvb [T, Hh, 256]");
-  TORCH_CHECK(kr.size(1) == kD - kDN && kr.stride(1) == 1, "mla_prefill: kr [T, 64]");
+  const int DN = q.size(2) - 64, DV = kvb.size(2) - DN;
+  TORCH_CHECK((DN == 128 || DN == 192) && q.stride(2) == 1, "mla_prefill: q [T, Hh, 192 | 256] (nope 128 | 192 + rope 64)");
+  TORCH_CHECK(DV % kDV == 0 && DV > 0 && DV <= 512 && kvb.stride(2) == 1, "mla_prefill: kvb [T, Hh, nope + v], v % 128");
+  TORCH_CHECK(kr.size(1) == 64 && kr.stride(1) == 1, "mla_prefill: kr [T, 64]");
   const int nseq = cu_seqlens.size(0) - 1;
   if (nseq == 0 || max_len == 0) return;
   PrefillArgs p;
   p.q = (const __nv_bfloat16*)q.data_ptr(); p.q_tok_stride = q.stride(0); p.q_head_stride = q.stride(1);
   p.kvb = (const __nv_bfloat16*)kvb.data_ptr(); p.kvb_tok_stride = kvb.stride(0); p.kvb_head_stride = kvb.stride(1);
   p.kr = (const __nv_bfloat16*)kr.data_ptr(); p.kr_tok_stride = kr.stride(0);
-  p.cu_seqlens = cu_seqlens.data_ptr<int>(); p.nseq = nseq; p.Hh = Hh;
+  p.cu_seqlens = cu_seqlens.data_ptr<int>(); p.nseq = nseq; p.Hh = Hh; p.DV = DV;
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.out_q = (uint8_t*)opt_ptr(out_q); p.out_s = (uint8_t*)opt_ptr(out_s); p.out_bf16 = (__nv_bfloat16*)opt_ptr(out_bf16);
-  const size_t smem = (size_t)(2 * kBK * kKS + 2 * kBK * kVS + kBQ * kKS) * 2;
-  moet_allow_max_smem(mla_prefill_kernel);
   auto stream = at::cuda::getCurrentCUDAStream();
-  dim3 grid((max_len + kBQ - 1) / kBQ, Hh, nseq);
-  mla_prefill_kernel<<<grid, 256, smem, stream>>>(p);
+  dim3 grid((max_len + kBQ - 1) / kBQ, Hh * (DV / kDV), nseq);
+  auto launch = [&](auto dn) {
+    constexpr int kDN = decltype(dn)::value, kKS = kDN + 64 + 8;
+    const size_t smem = (size_t)(2 * kBK * kKS + 2 * kBK * kVS + kBQ * kKS) * 2;
+    moet_allow_max_smem(mla_prefill_kernel<kDN>);
+    mla_prefill_kernel<kDN><<<grid, 256, smem, stream>>>(p);
+  };
+  if (DN == 128) launch(std::integral_constant<int, 128>{});
+  else launch(std::integral_constant<int, 192>{});
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

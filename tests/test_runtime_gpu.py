@@ -123,3 +123,32 @@ def test_tp_shard_shapes_run_on_one_gpu(tp, ep):
     out = llm.generate([_prompt(300, 5)], SamplingParams(max_tokens=6, ignore_eos=True))
     assert len(out[0].outputs[0].token_ids) == 6
     llm.runner.check_status("tp shard shapes")
+
+
+def test_glm_head_dims_engine():
+    """GLM-5.x attention dims (q/k nope 192, v 256, 64-wide rope) with the DSA indexer:
+    non-absorbed prefill (two value chunks per head), absorbed decode with the 256-wide
+    W_UV combine; prefill logits and greedy decode track the fp32 reference and the
+    CUDA graph equals eager."""
+    from vllm_moet_b200.config import glm52_config
+    cfg = glm52_config(num_layers=3, hidden=1024, vocab=2048, num_experts=16, moe_intermediate=256,
+                       dense_intermediate=512, num_dense_layers=1, num_heads=8, q_lora_rank=256, top_k=4,
+                       index_heads=8, index_topk=2048)
+    assert (cfg.qk_nope_dim, cfg.v_head_dim) == (192, 256)
+    glm = LLM(cfg, device="cuda", num_speculative_tokens=2, max_model_len=1024, max_num_seqs=4)
+    p = _prompt(150, 31)            # > 128 tokens: two query tiles in the prefill kernel
+    sp = SamplingParams(max_tokens=8, ignore_eos=True)
+    out = glm.generate([p], sp)[0].outputs[0].token_ids
+    cs = reference.rope_cos_sin(glm.cfg, 512, "cuda")
+    toks = list(p)
+    for i, tok in enumerate(out):
+        lg, _ = reference.forward(glm.mw, torch.tensor(toks, device="cuda"), torch.arange(len(toks), device="cuda"), cs)
+        row = lg[-1]
+        assert float(row[tok]) >= float(row.max()) - 0.5 * (float(row.std()) + 1e-6), (i, tok, int(row.argmax()))
+        toks.append(tok)
+    glm.ecfg.cuda_graphs = False
+    try:
+        assert glm.generate([p], sp)[0].outputs[0].token_ids == out
+    finally:
+        glm.ecfg.cuda_graphs = True
+    glm.runner.check_status("glm dims")
