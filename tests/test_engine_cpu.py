@@ -55,3 +55,34 @@ def test_env_aliases(monkeypatch):
     monkeypatch.setenv("VLLM_MOE_W2_GATE_TAU", "0.7")
     c = MoetConfig.from_env()
     assert c.prefill_t == 128 and c.delta is True and c.gate_tau == 0.7
+
+
+def test_trace_env_aliases(monkeypatch):
+    from vllm_moet_b200.config import MoetConfig
+    monkeypatch.setenv("VLLM_PREFILL_TIMERS_FLUSH", "16")
+    monkeypatch.setenv("VLLM_MOE_W2_DELTA_TRACE", "2")
+    monkeypatch.setenv("VLLM_MOE_W2_GATE_FIRE_TIMING", "1")
+    monkeypatch.setenv("VLLM_MOE_W2_GATE_DUMP", "/tmp/g.jsonl")
+    m = MoetConfig.from_env()
+    assert (m.prefill_timers_flush, m.delta_trace, m.gate_fire_timing, m.gate_dump) == (16, 2, True, "/tmp/g.jsonl")
+
+
+def test_delta_trace_counts():
+    import torch
+    from vllm_moet_b200.utils.observability import DeltaTrace
+
+    class FakeDelta:
+        L, E = 2, 4
+        mirror = torch.tensor([[0, -1, -1, -1], [-1, 1, -1, -1]])
+        stats = {"fetched_rows": 2, "evictions": 0}
+
+        def resident(self, li, e):
+            return int(self.mirror[li, e]) >= 0
+    lines = []
+    t = DeltaTrace(level=2, every=2, sink=lines.append)
+    d = FakeDelta()
+    t.step(d, {(0, 0): 3, (0, 1): 1})
+    t.step(d, {(1, 1): 2, (1, 2): 2})
+    snap = t.snapshot(d)
+    assert snap["hit_rate_distinct"] == 0.5 and snap["hit_rate_tokens"] == 5 / 8
+    assert snap["coverage"] == 2 / 8 and snap["fp4_per_layer"] == [1, 1] and len(lines) == 1

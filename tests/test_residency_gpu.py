@@ -127,3 +127,32 @@ def test_split_fp4_delta_and_gate(resident_tokens, monkeypatch):
         assert float(row[tok]) >= float(row.max()) - 0.5 * (float(row.std()) + 1e-6), (tok, int(row.argmax()))
         seq.append(tok)
     loud.shutdown()
+
+
+def test_traces_and_dumps(tmp_path, monkeypatch):
+    """Prefill span timers, routing capture, the delta trace / precision-map dump and the
+    gate JSONL with fire timing, all switched on by the reference's env names."""
+    import json
+    import numpy as np
+    monkeypatch.setenv("VLLM_PREFILL_TIMERS_FLUSH", "4")
+    monkeypatch.setenv("VLLM_MOE_W2_DELTA_TRACE", "2")
+    monkeypatch.setenv("VLLM_MOE_W2_DELTA_DUMP", str(tmp_path / "prec.json"))
+    monkeypatch.setenv("VLLM_MOE_W2_DELTA_CAPTURE", str(tmp_path / "routes.npy"))
+    monkeypatch.setenv("VLLM_MOE_W2_GATE_FIRE_TIMING", "1")
+    monkeypatch.setenv("VLLM_MOE_W2_GATE_DUMP", str(tmp_path / "gate.jsonl"))
+    llm = LLM(_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=512, max_num_seqs=2,
+              delta_slots=48, gate=True)
+    llm.gate.tau = 2.0
+    llm.generate(_prompts(), SamplingParams(max_tokens=6, ignore_eos=True))
+    summary = llm.timers.summary()
+    assert {"prefill", "prefill.attention", "prefill.moe"} <= set(summary) and summary["prefill"]["total_ms"] > 0
+    llm.shutdown()
+    prec = json.loads((tmp_path / "prec.json").read_text())
+    assert prec["delta"]["tier"] == "fp4-direct8" and len(prec["delta"]["resident"]) > 0
+    assert 0 < prec["trace"]["coverage"] <= 1 and len(prec["trace"]["fp4_per_layer"]) == 3
+    routes = np.load(tmp_path / "routes.npy")
+    assert routes.ndim == 3 and routes.shape[1] == 3 and routes.shape[0] == llm._decode_steps
+    rows = [json.loads(x) for x in (tmp_path / "gate.jsonl").read_text().splitlines()]
+    assert len(rows) == llm._decode_steps and any(r["fired"] > 0 for r in rows)
+    fired = [it for r in rows for it in r["iters"]]
+    assert fired and all(it["promote_ms"] >= 0 and it["replay_ms"] > 0 for it in fired)

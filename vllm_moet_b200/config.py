@@ -221,6 +221,13 @@ class MoetConfig:
     store_threads: int = 8
     planes_cache: Optional[str] = None
     ckpt_id: Optional[str] = None
+    # tracing and dumps
+    prefill_timers_flush: int = 0       # CUDA-event spans of prefill, resolved every N spans (0 = off)
+    delta_trace: int = 0                # 1: delta coverage / hit-rate line; 2: + per-layer FP4 histogram
+    delta_dump: Optional[str] = None    # atomic JSON precision map (which expert sits in which tier)
+    delta_capture: Optional[str] = None  # .npy of per-step routed expert ids
+    gate_fire_timing: bool = False      # promote / replay milliseconds per gate iteration
+    gate_dump: Optional[str] = None     # JSONL: one row per gate evaluation
 
     ENV_ALIASES = {
         "prefill_t": "VLLM_MOE_W2_PREFILL_T",
@@ -253,6 +260,12 @@ class MoetConfig:
         "store_threads": "VLLM_MOE_W2_STORE_THREADS",
         "planes_cache": "VLLM_MOE_W2_PLANES_CACHE",
         "ckpt_id": "VLLM_MOE_W2_CKPT_ID",
+        "prefill_timers_flush": "VLLM_PREFILL_TIMERS_FLUSH",
+        "delta_trace": "VLLM_MOE_W2_DELTA_TRACE",
+        "delta_dump": "VLLM_MOE_W2_DELTA_DUMP",
+        "delta_capture": "VLLM_MOE_W2_DELTA_CAPTURE",
+        "gate_fire_timing": "VLLM_MOE_W2_GATE_FIRE_TIMING",
+        "gate_dump": "VLLM_MOE_W2_GATE_DUMP",
     }
 
     def __post_init__(self):

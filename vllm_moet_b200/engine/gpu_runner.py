@@ -17,6 +17,7 @@ Prefill replaces the absorbed attention with the non-absorbed flash kernel.
 """
 from __future__ import annotations
 
+import contextlib
 import math
 from dataclasses import dataclass
 from typing import Optional
@@ -128,6 +129,7 @@ class NativeRunner:
         self.debug_finite = os.environ.get("MOET_DEBUG_FINITE", "0") == "1"
         self.branches = os.environ.get("MOET_BRANCHES", "1") != "0"
         self.gemv_stream = os.environ.get("MOET_GEMV_STREAM", "1") != "0"
+        self.timers = None          # SpanTimers of prefill components (VLLM_PREFILL_TIMERS_FLUSH)
         # token count from which dense linears run on the tcgen05 GEMM (128-token tiles)
         self.tc_min_t = int(os.environ.get("MOET_TC_MIN_T", "16"))
         # decode expert tiles: 8-token pairs up to this many routed rows, 16-token pairs above
@@ -586,10 +588,14 @@ class NativeRunner:
         self._fused = self.ar is not None and ctx.mode == "decode" and self.ar.fits(ctx.T, H)
         self._decode = ctx.mode == "decode"
         x2 = self.ws.get("x_mid", (ctx.T, H), torch.bfloat16)
-        self._attention(lw, x, ctx, cache, li, x2)
+        timed = self.timers is not None and ctx.mode == "prefill"
+        with self.timers.span("prefill.attention") if timed else contextlib.nullcontext():
+            self._attention(lw, x, ctx, cache, li, x2)
         self._check(f"attention[{li}] ({ctx.mode})", x2)
         x3 = self.ws.get("x_a" if li % 2 == 0 else "x_b", (ctx.T, H), torch.bfloat16)
-        self._ffn(lw, x2, ctx, x3)
+        with (self.timers.span("prefill.moe" if self.cfg.is_moe_layer(li) else "prefill.dense_ffn") if timed
+              else contextlib.nullcontext()):
+            self._ffn(lw, x2, ctx, x3)
         self._check(f"ffn[{li}] ({ctx.mode})", x3)
         return x3
 

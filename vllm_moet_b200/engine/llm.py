@@ -10,6 +10,7 @@ emitted tokens and acceptance counts (pinned D2H).
 """
 from __future__ import annotations
 
+import contextlib
 import itertools
 import time
 from collections import deque
@@ -115,6 +116,7 @@ class LLM:
             self.delta = self.gate = None
             if delta_slots:
                 self._attach_delta(delta_slots, gate)
+            self._attach_tracing()
             self._DecodeState = DecodeState
             self._states = {}
             self._pin_active = None
@@ -122,6 +124,37 @@ class LLM:
             from .torch_runner import TorchRunner
             self.blocks = None
             self.runner = TorchRunner(self.mw, self.k, max_model_len, self.device, tp_group=tp_group)
+
+    def _attach_tracing(self):
+        """Prefill span timers, routing capture, delta trace / dump and the gate JSONL
+        (reference env names: VLLM_PREFILL_TIMERS_FLUSH, VLLM_MOE_W2_DELTA_TRACE / _DUMP /
+        _CAPTURE, VLLM_MOE_W2_GATE_FIRE_TIMING / _DUMP)."""
+        from ..utils import observability as obs
+        m = self.ecfg.moet
+        self.timers = obs.SpanTimers(flush_every=m.prefill_timers_flush) if m.prefill_timers_flush > 0 else None
+        self.runner.timers = self.timers
+        self.routing = obs.RoutingCapture() if m.delta_capture else None
+        self.delta_trace = (obs.DeltaTrace(level=m.delta_trace, every=m.kpi_every)
+                            if m.delta_trace and self.delta is not None else None)
+        self.gate_log = obs.JsonlWriter(m.gate_dump) if m.gate_dump and self.gate is not None else None
+        self._decode_steps = 0
+
+    def dump_traces(self):
+        """Write the configured dumps now (also done by shutdown)."""
+        from ..residency.fsutil import atomic_write_json
+        from ..utils import observability as obs
+        m = self.ecfg.moet
+        if m.delta_dump:
+            d = {"base": obs.precision_map(self.cache) if getattr(self, "cache", None) is not None else None,
+                 "delta": obs.precision_map(self.delta, "fp4-split" if getattr(self.delta, "split", False)
+                                            else "fp4-direct8") if getattr(self, "delta", None) is not None else None}
+            if getattr(self, "delta_trace", None) is not None:
+                d["trace"] = self.delta_trace.snapshot(self.delta)
+            atomic_write_json(m.delta_dump, d)
+        if getattr(self, "routing", None) is not None:
+            self.routing.save(m.delta_capture)
+        if getattr(self, "timers", None) is not None:
+            obs.log.info("[moet] prefill timers: %s", self.timers.summary())
 
     def _resident_hardstop(self, cfg, tp, ep, num_layers):
         """Refuse early when fully resident experts cannot fit beside a KV floor and
@@ -147,7 +180,13 @@ class LLM:
         raise NotImplementedError("reload_weights is not supported with 2-bit experts; build a new LLM")
 
     def shutdown(self):
-        """Stop the residency managers (tiers first), then release stores and peer buffers."""
+        """Write the configured dumps, stop the residency managers (tiers first), then
+        release stores and peer buffers."""
+        if hasattr(self, "_decode_steps"):
+            self.dump_traces()
+        if getattr(self, "gate_log", None) is not None:
+            self.gate_log.close()
+            self.gate_log = None
         for tier in (getattr(self, "delta", None), getattr(self, "cache", None)):
             if tier is not None:
                 tier.close()
@@ -185,6 +224,15 @@ class LLM:
             if t is not None:
                 pairs += [(li, int(e)) for e in torch.unique(t).tolist()]
         return pairs
+
+    def _routed_token_counts(self, B):
+        """{(layer, expert): rows routed to it} of the last decode step."""
+        out = {}
+        for li, t in enumerate(self.runner.route_ids(B)):
+            if t is not None:
+                e, n = torch.unique(t, return_counts=True)
+                out.update({(li, int(a)): int(b) for a, b in zip(e.tolist(), n.tolist())})
+        return out
 
     def _attach_cache(self, slots, kind, store_dir, tp_group):
         """Routed experts from a host store through a GPU expert cache of `slots` slots,
@@ -341,7 +389,8 @@ class LLM:
             if adm:
                 st.block_table.copy_(bt_host, non_blocking=False)
                 bts = [bt_host[r.row].tolist() for r in adm]
-                firsts = runner.prefill([r.prompt for r in adm], bts, [r.row for r in adm], st).tolist()
+                with self.timers.span("prefill") if self.timers is not None else contextlib.nullcontext():
+                    firsts = runner.prefill([r.prompt for r in adm], bts, [r.row for r in adm], st).tolist()
                 now = time.perf_counter()
                 for r, f in zip(adm, firsts):
                     r.t_first = now
@@ -374,6 +423,9 @@ class LLM:
                 runner.decode_body(st)
             if self.delta is not None:
                 self._delta_step(st, B, graph, kp1)
+            if self.routing is not None:
+                self.routing.record(runner.route_ids(B))
+            self._decode_steps += 1
             pin_out.copy_(st.out_tokens, non_blocking=True)
             pin_acc.copy_(st.n_acc, non_blocking=True)
             torch.cuda.current_stream().synchronize()
@@ -396,6 +448,8 @@ class LLM:
         pairs = self._routed_pairs(B)
         for li, e in pairs:
             self.delta.note_routed(li, [e])
+        if self.delta_trace is not None:
+            self.delta_trace.step(self.delta, self._routed_token_counts(B))
         if self.gate is not None:
             rows = torch.nonzero(st.active_rows).flatten()
             logits = self.runner.main_logits(B)
@@ -408,14 +462,29 @@ class LLM:
                 return logits[rows]
             # the step already ran once: score it, fire, replay (at most gate_fp_max times)
             score = self.gate.score(logits[rows])
-            fired = 0
+            score0, fired, iters = score, 0, []
+            timing = self.ecfg.moet.gate_fire_timing
             while fired < self.gate.fp_max and self.gate.should_fire(score):
                 promote = [p for p in self._routed_pairs(B) if not self.delta.resident(*p)][: self.gate.max_promote]
+                t0 = time.perf_counter()
                 if not promote or self.delta.promote(promote) == 0:
                     break
+                t1 = time.perf_counter()
+                if timing:
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
                 score = self.gate.score(run_step())
+                it = {"promoted": len(promote), "score": score}
+                if timing:
+                    e1.record()
+                    e1.synchronize()
+                    it.update(promote_ms=(t1 - t0) * 1e3, replay_ms=e0.elapsed_time(e1))
+                iters.append(it)
                 fired += 1
             self.delta.stats["gate_replays"] += fired
+            if self.gate_log is not None:
+                self.gate_log.write({"step": self._decode_steps, "score": score0, "tau": self.gate.tau,
+                                     "fired": fired, "final_score": score, "iters": iters})
         else:
             self.delta.tick()
         self.delta.step_end()

@@ -100,10 +100,66 @@ class RoutingCapture:
         os.replace(tmp, path)
 
 
-def precision_map(cache) -> dict:
-    """{"L": .., "E": .., "resident": [[layer, expert, slot], ...]} of an ExpertCache."""
+def precision_map(cache, tier: str = "base-2bit") -> dict:
+    """{"L": .., "E": .., "tier": .., "resident": [[layer, expert, slot], ...]} of an ExpertCache."""
     res = [[int(li), int(e), int(cache.mirror[li, e])] for li, e in (cache.mirror >= 0).nonzero().tolist()]
-    return {"L": cache.L, "E": cache.E, "tier": "base-2bit", "resident": res}
+    return {"L": cache.L, "E": cache.E, "tier": tier, "resident": res}
+
+
+class DeltaTrace:
+    """Delta-tier coverage and hit rates (reference: VLLM_MOE_W2_DELTA_TRACE, P:9718-9820).
+    Per decode step: the routed (layer, expert) pairs and how many of them the FP4
+    tier served (distinct pairs, and weighted by the tokens routed to them)."""
+
+    def __init__(self, level: int = 1, every: int = 500, sink=None):
+        self.level, self.every = level, max(1, every)
+        self.sink = sink or log.info
+        self.steps = 0
+        self.c = collections.Counter()
+
+    def step(self, delta, routed_tokens: Dict[tuple, int]):
+        self.steps += 1
+        for (li, e), n in routed_tokens.items():
+            hit = delta.resident(li, e)
+            self.c["pairs"] += 1
+            self.c["pair_hits"] += int(hit)
+            self.c["tokens"] += n
+            self.c["token_hits"] += n if hit else 0
+        if self.steps % self.every == 0:
+            self.sink(self.line(delta))
+
+    def snapshot(self, delta) -> dict:
+        resident = int((delta.mirror >= 0).sum())
+        d = {"steps": self.steps, "coverage": resident / max(1, delta.L * delta.E), "resident": resident,
+             "hit_rate_distinct": self.c["pair_hits"] / max(1, self.c["pairs"]),
+             "hit_rate_tokens": self.c["token_hits"] / max(1, self.c["tokens"]),
+             "promoted_rows": int(delta.stats["fetched_rows"]), "evictions": int(delta.stats["evictions"])}
+        if self.level >= 2:
+            d["fp4_per_layer"] = (delta.mirror >= 0).sum(dim=1).tolist()
+        return d
+
+    def line(self, delta) -> str:
+        d = self.snapshot(delta)
+        s = (f"[moet] delta: steps {d['steps']} coverage {100 * d['coverage']:.1f}% ({d['resident']} experts) "
+             f"hit distinct {100 * d['hit_rate_distinct']:.1f}% tokens {100 * d['hit_rate_tokens']:.1f}% "
+             f"promoted {d['promoted_rows']} evicted {d['evictions']}")
+        if self.level >= 2:
+            s += f" per-layer {d['fp4_per_layer']}"
+        return s
+
+
+class JsonlWriter:
+    """Append-only JSON lines (one object per line, flushed per row)."""
+
+    def __init__(self, path: str):
+        self.path = path
+        self.f = open(path, "a", buffering=1)
+
+    def write(self, row: dict):
+        self.f.write(json.dumps(row, sort_keys=True) + "\n")
+
+    def close(self):
+        self.f.close()
 
 
 class SpanTimers:
