@@ -351,3 +351,61 @@ def test_split_delta_coupling_protects_the_base(tmp_path):
                 assert int(base.slot_table[li, e]) == int(base.mirror[li, e])
     finally:
         delta.close()
+
+
+def test_storm_invariants_hold_every_iteration(tmp_path):
+    """Random promotions, manager-thread prefetches, routed pins, injected pack read
+    faults and split-FP4 promotions over a tiered base cache; the residency
+    invariants (pool bytes, mirror / owner / free / slot-table coherence, split
+    coupling, store integrity) are checked after every iteration."""
+    import random
+    from vllm_moet_b200.residency.delta import DeltaTier, split_layout
+    rnd = random.Random(1234)
+    st = make_store("tiered", L, E, SB, dir=str(tmp_path), ckpt_id="storm", arena_rows=7)
+    fill(st)
+    base = ExpertCache(st, L, E, SB, 9, device="cpu", policy="freq", manager=True)
+    H = I = 64
+    sbq = split_layout(H, I)[0]
+    drows = [torch.randint(0, 256, (E, sbq), generator=torch.Generator().manual_seed(50 + li), dtype=torch.uint8)
+             for li in range(L)]
+    delta = DeltaTier(drows, H, I, 4, device="cpu", policy="lru", split=True)
+    delta.couple(base)
+    failures = 0
+    try:
+        for it in range(150):
+            base.step_begin()
+            op = rnd.random()
+            pairs = [(rnd.randrange(L), rnd.randrange(E)) for _ in range(rnd.randint(1, 4))]
+            try:
+                if op < 0.35:
+                    base.promote(pairs)
+                elif op < 0.55:
+                    base.request_prefetch(pairs)
+                elif op < 0.70:
+                    delta.promote(pairs[:2])
+                elif op < 0.80:
+                    li = rnd.randrange(L)
+                    base.ensure_resident(li, [rnd.randrange(E) for _ in range(3)])
+                elif op < 0.90:
+                    for li, e in pairs:
+                        base.note_routed(li, [e])
+                else:
+                    st.inject_read_faults(rnd.choice([1, 2, 3]))
+                    base.promote(pairs)
+            except FetchError:
+                failures += 1
+            finally:
+                st.inject_read_faults(0)
+            assert base.wait_idle(10)
+            base.step_end()
+            delta.step_end()
+            base.check_invariants(host_row=lambda li, e: layer_rows(li)[e])
+            delta.check_invariants(host_row=lambda li, e: drows[li][e], base=base)
+        for li in range(L):                      # store integrity after the storm
+            got = st.rows_for(li, list(range(E)))
+            assert not got.failed and all(torch.equal(r, layer_rows(li)[e]) for e, r in enumerate(got.rows))
+        assert base.stats["evictions"] > 0 and delta.stats["fetched_rows"] > 0 and failures > 0
+    finally:
+        delta.close()
+        base.close()
+        st.release()

@@ -255,6 +255,42 @@ class ExpertCache:
         """Safe point: returns when no promotion is queued or running."""
         return self._idle.wait(timeout)
 
+    # ------------------------------------------------------------------ invariants
+    def check_invariants(self, host_row=None, base=None) -> None:
+        """Residency invariants (reference storm / stress checks I1-I5), raising
+        AssertionError on the first violation.  Call at a safe point (no promotion
+        in flight).
+        I1 every resident slot holds the bytes of its host row (``host_row(li, e)``);
+        I2 mirror, owner and free list are one bijection: mirror[li, e] = s exactly
+           when owner[s] = (li, e), a free slot has no owner, no slot is both;
+        I4 the device slot table (what the kernels dispatch on) equals the mirror;
+        I5 with ``base`` (split-FP4 coupling): every resident expert here is resident there."""
+        with self.lock:
+            seen = set()
+            for s, own in enumerate(self.owner):
+                if own is None:
+                    continue
+                li, e = own
+                assert int(self.mirror[li, e]) == s, f"I2: owner[{s}] = {own} but mirror = {int(self.mirror[li, e])}"
+                assert own not in seen, f"I2: {own} owns two slots"
+                seen.add(own)
+            for li, e in (self.mirror >= 0).nonzero().tolist():
+                s = int(self.mirror[li, e])
+                assert self.owner[s] == (li, e), f"I2: mirror[{li},{e}] = {s} but owner = {self.owner[s]}"
+            free = set(self.free)
+            assert len(free) == len(self.free), "I2: a slot is free twice"
+            assert all(self.owner[s] is None for s in free), "I2: a free slot has an owner"
+            assert len(free) + len(seen) == self.n_slots, "I2: a slot is neither free nor owned"
+            table = self.slot_table.cpu()
+            assert torch.equal(table, self.mirror.to(table.dtype)), "I4: device slot table != mirror"
+            if host_row is not None:
+                for li, e in seen:
+                    s = int(self.mirror[li, e])
+                    assert torch.equal(self.pool[s].cpu(), host_row(li, e).cpu()), f"I1: slot {s} != host row {li},{e}"
+            if base is not None:
+                for li, e in seen:
+                    assert base.resident(li, e), f"I5: ({li}, {e}) has an FP4 slot but no resident base"
+
     # ------------------------------------------------------------------ heat
     def dump_heat(self, path: str):
         with self.lock:
