@@ -55,3 +55,31 @@ def _sp(rank, world):
 
 def test_sp_prefill_attention():
     assert max(run_ranks(_sp, 2)) < 1e-5
+
+
+def _sp_engine(rank, world):
+    """SP prefill through the engine: each rank prefills its chunk of the prompt; the
+    first token, the MTP drafts and the decode that follows equal the single-rank engine."""
+    import torch.distributed as dist
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256, sp_group=dist.group.WORLD)
+    prompts = [list(range(5, 5 + 37)), [7, 11, 13, 17, 19, 23, 29]]       # uneven chunks, padded tail
+    out = llm.generate(prompts, SamplingParams(max_tokens=8, ignore_eos=True))
+    return [o.outputs[0].token_ids for o in out]
+
+
+def test_sp_prefill_engine_matches_single_rank():
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    one = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+    prompts = [list(range(5, 5 + 37)), [7, 11, 13, 17, 19, 23, 29]]
+    want = [o.outputs[0].token_ids for o in one.generate(prompts, SamplingParams(max_tokens=8, ignore_eos=True))]
+    for got in run_ranks(_sp_engine, 3):            # 37 = 13 + 13 + 11 and 7 = 3 + 3 + 1: padded tails
+        assert got == want, (got, want)
+
+
+def test_sp_chunking():
+    from vllm_moet_b200.parallel.context import sp_chunk
+    assert [sp_chunk(10, 3, r) for r in range(3)] == [(4, 0, 4), (4, 4, 4), (4, 8, 2)]
+    assert sp_chunk(2, 4, 3) == (1, 3, 0)

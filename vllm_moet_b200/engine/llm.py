@@ -48,8 +48,11 @@ class LLM:
                  tensor_parallel_size: int = 1, tp_group=None, tp_rank: int = 0,
                  pipeline_parallel_size: int = 1, pp_group=None, pp_rank: int = 0, expert_cache_slots: int = 0,
                  delta_slots: int = 0, gate: Optional[bool] = None, expert_parallel: bool = False,
-                 expert_store: str = "pinned", expert_store_dir: Optional[str] = None, **model_overrides):
+                 expert_store: str = "pinned", expert_store_dir: Optional[str] = None, sp_group=None,
+                 **model_overrides):
         cfg = get_preset(model, **model_overrides) if isinstance(model, str) else model
+        if sp_group is not None and (tp_group is not None or pp_group is not None):
+            raise ValueError("sequence-parallel prefill runs on replicated weights (no TP / PP group)")
         self._mtp_requested = num_speculative_tokens > 0
         if num_layers is not None:
             cfg = cfg.replace(num_layers=num_layers)
@@ -123,7 +126,8 @@ class LLM:
         else:
             from .torch_runner import TorchRunner
             self.blocks = None
-            self.runner = TorchRunner(self.mw, self.k, max_model_len, self.device, tp_group=tp_group)
+            self.runner = TorchRunner(self.mw, self.k, max_model_len, self.device, tp_group=tp_group,
+                                      sp_group=sp_group)
 
     def _attach_tracing(self):
         """Prefill span timers, routing capture, delta trace / dump and the gate JSONL

@@ -11,13 +11,14 @@ from ..models.weights import ModelWeights
 
 
 class TorchRunner:
-    def __init__(self, mw: ModelWeights, k: int, max_len: int, device="cpu", tp_group=None):
+    def __init__(self, mw: ModelWeights, k: int, max_len: int, device="cpu", tp_group=None, sp_group=None):
         self.mw = mw
         self.k = k if mw.mtp is not None else 0
         self.dev = torch.device(device)
         self.cs = ref.rope_cos_sin(mw.cfg, max_len + 64, self.dev)
         self.rows = {}
         self.tp_group = tp_group        # tensor-parallel CPU ranks (gloo): sharded weights, all-reduced partials
+        self.sp_group = sp_group        # sequence-parallel prefill ranks: prompt chunks, gathered MLA latents
 
     def _row(self, r):
         return self.rows[r]
@@ -37,8 +38,13 @@ class TorchRunner:
             n = len(prompt)
             main, mtp = ref.RefKV(len(self.mw.layers)), ref.RefKV(1)
             toks = torch.tensor(prompt, device=self.dev)
-            logits, hid = ref.forward(self.mw, toks, torch.arange(n, device=self.dev), self.cs, main)
-            tgt = int(logits[-1].argmax())
+            if self.sp_group is not None:
+                from ..parallel.context import sp_prefill_forward
+                last, hid = sp_prefill_forward(self.mw, toks, self.cs, self.sp_group, main)
+                tgt = int(last.argmax())
+            else:
+                logits, hid = ref.forward(self.mw, toks, torch.arange(n, device=self.dev), self.cs, main)
+                tgt = int(logits[-1].argmax())
             drafts = []
             if self.k:
                 nxt = torch.tensor(prompt[1:] + [tgt], device=self.dev)

@@ -104,3 +104,72 @@ def sp_prefill_attention(q_local, k_local, v_local, scale, group):
     mask = torch.arange(W * Tc)[None, :] <= qpos[:, None]
     o, _ = partial_attention(q_local, k_all, v_all, scale, mask)
     return o
+
+
+# ---------------------------------------------------------------- SP prefill, model level
+def sp_chunk(n: int, world: int, rank: int) -> Tuple[int, int, int]:
+    """Prompt of n tokens over `world` ranks -> (chunk length Tc, first position, real tokens
+    on this rank).  Chunks are equal (the tail is padded); padding sits after every real
+    token, so causality keeps it out of every real row."""
+    Tc = -(-n // world)
+    lo = rank * Tc
+    return Tc, lo, max(0, min(n, lo + Tc) - lo)
+
+
+def sp_attention(cfg, lw, x_local: torch.Tensor, lo: int, cs: torch.Tensor, group, cache=None, li: int = 0):
+    """MLA attention for this rank's contiguous chunk (global positions lo..lo+Tc-1).
+    All-gathered per token: the compressed row only (normed latent + roped shared key,
+    kv_lora + rope values), not per-head K/V; every rank expands the gathered latents
+    itself.  With `cache`, the full sequence's K/V is stored for decode."""
+    from ..models import reference as ref
+    W, _ = _world(group)
+    Tc = x_local.shape[0]
+    Hh = lw.q_b.shape[0] // cfg.qk_head_dim
+    nope, rope, vd, lat = cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim, cfg.kv_lora_rank
+    pos = lo + torch.arange(Tc, device=x_local.device)
+    qkva = x_local.float() @ lw.qkv_a.dequant().t()
+    qa = ref.rms_norm(qkva[:, : cfg.q_lora_rank], lw.q_a_norm, cfg.rms_eps)
+    c = ref.rms_norm(qkva[:, cfg.q_lora_rank: cfg.q_lora_rank + lat], lw.kv_a_norm, cfg.rms_eps)
+    kr = ref.apply_rope(qkva[:, cfg.q_lora_rank + lat:], cs[pos])
+    row = torch.cat([c, kr], dim=-1)                                   # [Tc, lat + rope]
+    rows = _all_gather(row, group).reshape(W * Tc, lat + rope)         # the whole (padded) prompt
+    q = (qa @ lw.q_b.dequant().t()).view(Tc, Hh, nope + rope)
+    q_pe = ref.apply_rope(q[..., nope:].transpose(0, 1), cs[pos]).transpose(0, 1)
+    kvb = (rows[:, :lat] @ lw.kv_b.dequant().t()).view(W * Tc, Hh, nope + vd)
+    S = W * Tc
+    k = torch.cat([kvb[..., :nope], rows[:, None, lat:].expand(S, Hh, rope)], dim=-1).transpose(0, 1)
+    v = kvb[..., nope:].transpose(0, 1)
+    qf = torch.cat([q[..., :nope], q_pe], dim=-1).transpose(0, 1)       # [Hh, Tc, qk]
+    if cache is not None:
+        cache.k[li], cache.v[li] = k, v
+    s = (qf @ k.transpose(1, 2)) * (1.0 / math.sqrt(nope + rope))
+    s = s.masked_fill(torch.arange(S, device=s.device)[None, None, :] > pos[None, :, None], float("-inf"))
+    o = torch.softmax(s, dim=-1) @ v
+    return o.transpose(0, 1).reshape(Tc, Hh * vd) @ lw.o.dequant().t()
+
+
+def sp_prefill_forward(mw, tokens: torch.Tensor, cs: torch.Tensor, group, cache=None):
+    """Sequence-parallel prefill of one prompt (the full token list on every rank; each
+    rank computes its chunk).  -> (logits of the last real token [V], final normed
+    hidden of every real token [n, H], gathered on every rank).  `cache` (RefKV) gets the
+    full K/V of every layer, truncated to the real tokens."""
+    from ..models import reference as ref
+    cfg = mw.cfg
+    W, r = _world(group)
+    n = tokens.shape[0]
+    Tc, lo, _ = sp_chunk(n, W, r)
+    ids = torch.zeros(Tc, dtype=torch.long, device=tokens.device)
+    real = tokens[lo:lo + Tc]
+    ids[:real.shape[0]] = real
+    x = mw.embed[ids].float()
+    for li, lw in enumerate(mw.layers):
+        h = ref.rms_norm(x, lw.attn_norm, cfg.rms_eps)
+        x = x + sp_attention(cfg, lw, h, lo, cs, group, cache, li)
+        h = ref.rms_norm(x, lw.ffn_norm, cfg.rms_eps)
+        x = x + (ref.moe_block(cfg, lw, h) if lw.is_moe else ref.dense_ffn(cfg, lw, h))
+    hn = ref.rms_norm(x, mw.final_norm, cfg.rms_eps)
+    hid = _all_gather(hn, group).reshape(W * Tc, -1)[:n]
+    if cache is not None:
+        cache.truncate(n)
+    logits = hid[-1:] @ mw.lm_head.dequant().t()
+    return logits[0], hid
