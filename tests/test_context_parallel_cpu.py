@@ -83,3 +83,53 @@ def test_sp_chunking():
     from vllm_moet_b200.parallel.context import sp_chunk
     assert [sp_chunk(10, 3, r) for r in range(3)] == [(4, 0, 4), (4, 4, 4), (4, 8, 2)]
     assert sp_chunk(2, 4, 3) == (1, 3, 0)
+
+
+def _dcp_engine(rank, world, interleave):
+    import torch.distributed as dist
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256, dcp_group=dist.group.WORLD,
+              dcp_interleave=interleave)
+    prompts = [list(range(5, 5 + 37)), [7, 11, 13, 17, 19, 23, 29]]
+    out = llm.generate(prompts, SamplingParams(max_tokens=10, ignore_eos=True))
+    # a row kept open: which positions of each layer's K/V this rank holds
+    llm.runner.prefill([prompts[0]], [99])
+    for _ in range(3):
+        llm.runner.step([99])
+    st = llm.runner.rows[99]
+    held = [st["main"].pos[li].tolist() for li in range(len(st["main"].pos))]
+    return [o.outputs[0].token_ids for o in out], held, st["pos"]
+
+
+def test_dcp_engine_matches_single_rank():
+    """KV interleaved over 3 ranks in runs of 2 positions: prefill, MTP verify with
+    rejected drafts (truncation by position) and decode equal the single-rank engine;
+    each rank holds exactly the positions it owns and the shards tile the sequence."""
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    one = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+    prompts = [list(range(5, 5 + 37)), [7, 11, 13, 17, 19, 23, 29]]
+    want = [o.outputs[0].token_ids for o in one.generate(prompts, SamplingParams(max_tokens=10, ignore_eos=True))]
+    for il in (2,):
+        res = run_ranks(_dcp_engine, 3, il)
+        for rank, (got, held, _) in enumerate(res):
+            assert got == want, (il, got, want)
+            for layer in held:
+                assert all((p // il) % 3 == rank for p in layer)
+        n = res[0][2]
+        for li in range(len(res[0][1])):
+            # contiguous from 0, no position twice; the last verify step's drafts stay cached
+            # past `pos` until the next step truncates them, as in the single-rank cache
+            union = sorted(p for r in range(3) for p in res[r][1][li])
+            assert union == list(range(len(union))) and len(union) >= n, (il, li)
+
+
+def test_shard_kv_truncates_by_position():
+    from vllm_moet_b200.parallel.context import ShardKV
+    kv = ShardKV(1, world=2, rank=1, interleave=2)
+    pos = torch.arange(10)
+    kv.append(0, torch.arange(10.)[None, :, None], torch.arange(10.)[None, :, None], pos)
+    assert kv.pos[0].tolist() == [2, 3, 6, 7]
+    kv.truncate(7)
+    assert kv.pos[0].tolist() == [2, 3, 6] and kv.k[0].shape[1] == 3

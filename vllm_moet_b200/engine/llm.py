@@ -49,16 +49,20 @@ class LLM:
                  pipeline_parallel_size: int = 1, pp_group=None, pp_rank: int = 0, expert_cache_slots: int = 0,
                  delta_slots: int = 0, gate: Optional[bool] = None, expert_parallel: bool = False,
                  expert_store: str = "pinned", expert_store_dir: Optional[str] = None, sp_group=None,
-                 **model_overrides):
+                 dcp_group=None, dcp_interleave: int = 1, **model_overrides):
         cfg = get_preset(model, **model_overrides) if isinstance(model, str) else model
-        if sp_group is not None and (tp_group is not None or pp_group is not None):
-            raise ValueError("sequence-parallel prefill runs on replicated weights (no TP / PP group)")
+        if (sp_group is not None or dcp_group is not None) and (tp_group is not None or pp_group is not None):
+            raise ValueError("context parallelism here runs on replicated weights (no TP / PP group)")
+        if sp_group is not None and dcp_group is not None:
+            raise ValueError("choose one of sp_group (SP prefill) and dcp_group (DCP decode)")
         self._mtp_requested = num_speculative_tokens > 0
         if num_layers is not None:
             cfg = cfg.replace(num_layers=num_layers)
         if device is None:
             device = "cuda" if torch.cuda.is_available() else "cpu"
         self.device = torch.device(device)
+        if self.device.type == "cuda" and (sp_group is not None or dcp_group is not None):
+            raise NotImplementedError("SP prefill / DCP decode run on the CPU engine; the GPU runner has neither yet")
         if self.device.type == "cuda" and cfg.expert_scale != "ue8m0":
             cfg = cfg.replace(expert_scale="ue8m0")
         if self.device.type == "cuda" and cfg.dense_dtype != "fp8":
@@ -127,7 +131,7 @@ class LLM:
             from .torch_runner import TorchRunner
             self.blocks = None
             self.runner = TorchRunner(self.mw, self.k, max_model_len, self.device, tp_group=tp_group,
-                                      sp_group=sp_group)
+                                      sp_group=sp_group, dcp_group=dcp_group, dcp_interleave=dcp_interleave)
 
     def _attach_tracing(self):
         """Prefill span timers, routing capture, delta trace / dump and the gate JSONL

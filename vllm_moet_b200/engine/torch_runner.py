@@ -11,7 +11,8 @@ from ..models.weights import ModelWeights
 
 
 class TorchRunner:
-    def __init__(self, mw: ModelWeights, k: int, max_len: int, device="cpu", tp_group=None, sp_group=None):
+    def __init__(self, mw: ModelWeights, k: int, max_len: int, device="cpu", tp_group=None, sp_group=None,
+                 dcp_group=None, dcp_interleave: int = 1):
         self.mw = mw
         self.k = k if mw.mtp is not None else 0
         self.dev = torch.device(device)
@@ -19,13 +20,26 @@ class TorchRunner:
         self.rows = {}
         self.tp_group = tp_group        # tensor-parallel CPU ranks (gloo): sharded weights, all-reduced partials
         self.sp_group = sp_group        # sequence-parallel prefill ranks: prompt chunks, gathered MLA latents
+        self.dcp_group = dcp_group      # decode-context-parallel ranks: KV interleaved by position, LSE merge
+        self.dcp_interleave = dcp_interleave
 
     def _row(self, r):
         return self.rows[r]
 
     def _ctx(self):
         import contextlib
+        if self.dcp_group is not None:
+            from ..parallel.context import dcp_attention_fn
+            return ref.attention_context(dcp_attention_fn(self.dcp_group))
         return ref.tp_context(self.tp_group) if self.tp_group is not None else contextlib.nullcontext()
+
+    def _kv(self, n_layers: int):
+        if self.dcp_group is None:
+            return ref.RefKV(n_layers)
+        import torch.distributed as dist
+        from ..parallel.context import ShardKV
+        return ShardKV(n_layers, dist.get_world_size(self.dcp_group), dist.get_rank(self.dcp_group),
+                       self.dcp_interleave)
 
     @torch.no_grad()
     def prefill(self, prompts, rows):
@@ -36,7 +50,7 @@ class TorchRunner:
         firsts = []
         for prompt, r in zip(prompts, rows):
             n = len(prompt)
-            main, mtp = ref.RefKV(len(self.mw.layers)), ref.RefKV(1)
+            main, mtp = self._kv(len(self.mw.layers)), self._kv(1)
             toks = torch.tensor(prompt, device=self.dev)
             if self.sp_group is not None:
                 from ..parallel.context import sp_prefill_forward

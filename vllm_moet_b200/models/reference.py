@@ -48,6 +48,26 @@ class tp_context:
         _TP_GROUP = self.prev
 
 
+_ATTN_IMPL = None
+
+
+class attention_context:
+    """Run every decoder layer's attention through `fn` (same signature as
+    :func:`attention`), e.g. decode-context-parallel attention over a sharded KV."""
+
+    def __init__(self, fn):
+        self.fn = fn
+
+    def __enter__(self):
+        global _ATTN_IMPL
+        self.prev, _ATTN_IMPL = _ATTN_IMPL, self.fn
+        return self
+
+    def __exit__(self, *a):
+        global _ATTN_IMPL
+        _ATTN_IMPL = self.prev
+
+
 def _allreduce(x: torch.Tensor) -> torch.Tensor:
     if _TP_GROUP is not None:
         import torch.distributed as dist
@@ -208,7 +228,7 @@ def attention(cfg: ModelConfig, lw: LayerWeights, x: torch.Tensor, positions: to
 
 def decoder_layer(cfg, lw, x, positions, cs, cache=None, li=0):
     h = rms_norm(x, lw.attn_norm, cfg.rms_eps)
-    x = x + _allreduce(attention(cfg, lw, h, positions, cs, cache, li))
+    x = x + _allreduce((_ATTN_IMPL or attention)(cfg, lw, h, positions, cs, cache, li))
     h = rms_norm(x, lw.ffn_norm, cfg.rms_eps)
     return x + _allreduce(moe_block(cfg, lw, h) if lw.is_moe else dense_ffn(cfg, lw, h))
 

@@ -173,3 +173,68 @@ def sp_prefill_forward(mw, tokens: torch.Tensor, cs: torch.Tensor, group, cache=
         cache.truncate(n)
     logits = hid[-1:] @ mw.lm_head.dequant().t()
     return logits[0], hid
+
+
+# ---------------------------------------------------------------- DCP, model level
+class ShardKV:
+    """This rank's share of a sequence's per-layer K/V under decode context parallelism:
+    position p lives on rank (p // interleave) % world.  Entries keep their positions, so
+    truncation (rejected drafts) is by position.  Same interface as the oracle's RefKV."""
+
+    def __init__(self, n_layers: int, world: int, rank: int, interleave: int = 1):
+        self.world, self.rank, self.interleave = world, rank, interleave
+        self.k = [None] * n_layers        # [Hh, S_r, qk]
+        self.v = [None] * n_layers        # [Hh, S_r, vd]
+        self.pos = [None] * n_layers      # [S_r]
+
+    def owns(self, positions: torch.Tensor) -> torch.Tensor:
+        return (positions // self.interleave) % self.world == self.rank
+
+    def append(self, li: int, k: torch.Tensor, v: torch.Tensor, positions: torch.Tensor):
+        m = self.owns(positions)
+        k, v, p = k[:, m], v[:, m], positions[m]
+        if self.k[li] is None:
+            self.k[li], self.v[li], self.pos[li] = k, v, p
+        else:
+            self.k[li] = torch.cat([self.k[li], k], dim=1)
+            self.v[li] = torch.cat([self.v[li], v], dim=1)
+            self.pos[li] = torch.cat([self.pos[li], p])
+
+    def truncate(self, length: int):
+        for i in range(len(self.k)):
+            if self.k[i] is not None:
+                keep = self.pos[i] < length
+                self.k[i], self.v[i], self.pos[i] = self.k[i][:, keep], self.v[i][:, keep], self.pos[i][keep]
+
+
+def dcp_attention_fn(group):
+    """-> an attention function for the oracle's decoder layers (see
+    ``reference.attention_context``): q / K / V of the step's tokens are computed on
+    every rank, each rank appends the positions it owns to its ShardKV, attends over its
+    shard (causal by position) and the (o, lse) partials are LSE-merged across ranks."""
+    from ..models import reference as ref
+
+    def attn(cfg, lw, x, positions, cs, cache, li=0, heads=None):
+        Hh = heads or lw.q_b.shape[0] // cfg.qk_head_dim
+        T = x.shape[0]
+        nope, rope, vd, lat = cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim, cfg.kv_lora_rank
+        qkva = x.float() @ lw.qkv_a.dequant().t()
+        qa = ref.rms_norm(qkva[:, : cfg.q_lora_rank], lw.q_a_norm, cfg.rms_eps)
+        c = ref.rms_norm(qkva[:, cfg.q_lora_rank: cfg.q_lora_rank + lat], lw.kv_a_norm, cfg.rms_eps)
+        pcs = cs[positions]
+        kr = ref.apply_rope(qkva[:, cfg.q_lora_rank + lat:], pcs)
+        q = (qa @ lw.q_b.dequant().t()).view(T, Hh, nope + rope)
+        q_pe = ref.apply_rope(q[..., nope:].transpose(0, 1), pcs).transpose(0, 1)
+        kvb = (c @ lw.kv_b.dequant().t()).view(T, Hh, nope + vd)
+        k = torch.cat([kvb[..., :nope], kr[:, None, :].expand(T, Hh, rope)], dim=-1).transpose(0, 1)
+        cache.append(li, k, kvb[..., nope:].transpose(0, 1), positions)
+        qf = torch.cat([q[..., :nope], q_pe], dim=-1)                      # [T, Hh, qk]
+        ks, vs, ps = cache.k[li], cache.v[li], cache.pos[li]
+        s = torch.einsum("thd,hsd->ths", qf.float(), ks.float()) * (1.0 / math.sqrt(nope + rope))
+        s = s.masked_fill(ps[None, None, :] > positions[:, None, None], float("-inf"))
+        lse = torch.logsumexp(s, dim=-1)                                   # [T, Hh]; -inf: no key here
+        p = torch.exp(s - torch.where(torch.isinf(lse), torch.zeros_like(lse), lse)[..., None])
+        o = torch.einsum("ths,hsd->thd", p, vs.float())
+        o = lse_merge(_all_gather(o, group), _all_gather(lse, group))       # [T, Hh, vd]
+        return o.reshape(T, Hh * vd) @ lw.o.dequant().t()
+    return attn
