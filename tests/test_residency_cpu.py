@@ -409,3 +409,22 @@ def test_storm_invariants_hold_every_iteration(tmp_path):
         delta.close()
         base.close()
         st.release()
+
+
+def _gate_tp(rank, world, fail_rank, empty_rank):
+    import torch.distributed as dist
+    from vllm_moet_b200.residency import FetchError, gate_promote_consensus
+
+    def promote():
+        if rank == fail_rank:
+            raise FetchError("injected promotion failure")
+        return 0 if rank == empty_rank else 3
+    return gate_promote_consensus(promote, dist.group.WORLD)
+
+
+def test_gate_promote_consensus_fail_safe():
+    assert all(run_ranks(_gate_tp, 3, -1, -1))                  # everyone promoted -> everyone replays
+    assert not any(run_ranks(_gate_tp, 3, 1, -1))               # one failed read -> nobody replays
+    assert all(run_ranks(_gate_tp, 3, -1, 2))                   # nothing new on one rank still replays together
+    from vllm_moet_b200.residency import gate_promote_consensus
+    assert gate_promote_consensus(lambda: 2) and not gate_promote_consensus(lambda: 0)

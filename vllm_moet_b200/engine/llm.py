@@ -61,6 +61,7 @@ class LLM:
         if device is None:
             device = "cuda" if torch.cuda.is_available() else "cpu"
         self.device = torch.device(device)
+        self._tp_group = tp_group
         if self.device.type == "cuda" and (sp_group is not None or dcp_group is not None):
             raise NotImplementedError("SP prefill / DCP decode run on the CPU engine; the GPU runner has neither yet")
         if self.device.type == "cuda" and cfg.expert_scale != "ue8m0":
@@ -453,6 +454,7 @@ class LLM:
         """After a decode step: feed routing to the delta tier's frequency policy and,
         with the confidence gate, promote this step's routed experts to FP4 and
         replay the step while the verify rows are not confident."""
+        from ..residency import gate_promote_consensus
         pairs = self._routed_pairs(B)
         for li, e in pairs:
             self.delta.note_routed(li, [e])
@@ -466,7 +468,11 @@ class LLM:
 
             def run_step():
                 st.restore(snap)
-                step()
+                if self.cache is not None:      # base misses met by the replayed step are repaired too
+                    self.cache.wait_idle()
+                    self.replay.run(step, lambda: st.restore(snap), lambda: self.runner.route_ids(B))
+                else:
+                    step()
                 return logits[rows]
             # the step already ran once: score it, fire, replay (at most gate_fp_max times)
             score = self.gate.score(logits[rows])
@@ -475,7 +481,9 @@ class LLM:
             while fired < self.gate.fp_max and self.gate.should_fire(score):
                 promote = [p for p in self._routed_pairs(B) if not self.delta.resident(*p)][: self.gate.max_promote]
                 t0 = time.perf_counter()
-                if not promote or self.delta.promote(promote) == 0:
+                # fail-safe: a failed host read on any TP rank means no rank replays
+                if not gate_promote_consensus(lambda: self.delta.promote(promote) if promote else 0,
+                                              self._tp_group, self.device):
                     break
                 t1 = time.perf_counter()
                 if timing:

@@ -2,7 +2,7 @@
 cache with in-graph miss counting and replay, the confidence gate, the
 speculation guard and the routing prefetchers."""
 from .control import (ConfidenceGate, DraftAffinity, LookaheadPrefetcher, ReplayEngine, SpecGuard,  # noqa: F401
-                      gate_fire_floor, pp_gate_barrier)
+                      gate_fire_floor, pp_gate_barrier, gate_promote_consensus)
 from .identity import checkpoint_id, identity_fields, rank_suffix  # noqa: F401
 from .planes_cache import PlanesCache  # noqa: F401
 from .stores import (MmapPackStore, PinnedHostStore, RowBatch, TieredPackStore, make_store,  # noqa: F401

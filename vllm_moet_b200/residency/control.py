@@ -264,3 +264,23 @@ def pp_gate_barrier(fire_on_last: bool, promote, tp_group=None, pp_group=None, d
         if g is not None:
             dist.all_reduce(t, op=dist.ReduceOp.MIN, group=g)
     return bool(int(t.item()))
+
+
+def gate_promote_consensus(promote, tp_group=None, device="cpu") -> bool:
+    """Confidence-gate promotion under tensor parallelism (reference: the gate is
+    fail-safe before its collective, P:21396-21404, P:18947-18957).  Every rank runs
+    `promote()` (-> rows promoted; FetchError on a failed host read); the ranks agree
+    (MIN of an ok flag, MAX of "promoted something") before anyone replays.  Returns
+    True only when every rank succeeded and at least one promoted, i.e. when all ranks
+    replay the step together; otherwise nobody replays and the step stands."""
+    ok, n = 1, 0
+    try:
+        n = int(promote() or 0)
+    except FetchError:
+        ok = 0
+    if tp_group is None:
+        return bool(ok and n > 0)
+    import torch.distributed as dist
+    t = torch.tensor([ok, -min(n, 1)], dtype=torch.int32, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN, group=tp_group)   # [min ok, -max promoted]
+    return bool(int(t[0]) == 1 and int(t[1]) < 0)
