@@ -61,7 +61,7 @@ class LLM:
         if device is None:
             device = "cuda" if torch.cuda.is_available() else "cpu"
         self.device = torch.device(device)
-        self._tp_group = tp_group
+        self._tp_group, self._pp_group = tp_group, pp_group
         if self.device.type == "cuda" and (sp_group is not None or dcp_group is not None):
             raise NotImplementedError("SP prefill / DCP decode run on the CPU engine; the GPU runner has neither yet")
         if self.device.type == "cuda" and cfg.expert_scale != "ue8m0":
@@ -473,7 +473,12 @@ class LLM:
                     self.replay.run(step, lambda: st.restore(snap), lambda: self.runner.route_ids(B))
                 else:
                     step()
-                return logits[rows]
+                return logits[rows] if logits is not None else None     # no head before the last PP stage
+            if self._pp_group is not None:
+                fired = self._pp_gate(B, run_step, lambda: self.gate.score(logits[rows]))
+                self.delta.stats["gate_replays"] += fired
+                self.delta.step_end()
+                return
             # the step already ran once: score it, fire, replay (at most gate_fp_max times)
             score = self.gate.score(logits[rows])
             score0, fired, iters = score, 0, []
@@ -504,6 +509,31 @@ class LLM:
         else:
             self.delta.tick()
         self.delta.step_end()
+
+    def _pp_gate(self, B, run_step, score_fn) -> int:
+        """The gate under pipeline parallelism: only the last stage has the verify logits,
+        every stage owns its layers' experts.  Per round, the last stage's fire decision is
+        broadcast, every stage promotes its own routed experts, the outcome is agreed
+        (TP, then PP; fail closed), and then every stage replays the step together (its
+        sends / receives pair up).  -> replays."""
+        from ..residency import FetchError, pp_gate_barrier
+        last = self.runner.last_stage
+        score = score_fn() if last else 0.0
+        fired = 0
+        while fired < self.gate.fp_max:
+            fire = bool(last and self.gate.should_fire(score))
+
+            def promote():
+                pairs = [p for p in self._routed_pairs(B) if not self.delta.resident(*p)][: self.gate.max_promote]
+                if pairs and self.delta.promote(pairs) == 0:
+                    raise FetchError("nothing promoted")
+            if not pp_gate_barrier(fire, promote, tp_group=self._tp_group, pp_group=self._pp_group,
+                                   device=self.device):
+                break
+            out = run_step()
+            score = self.gate.score(out) if last else 0.0
+            fired += 1
+        return fired
 
     def _finish_row(self, r, rows):
         rows[r.row] = None
