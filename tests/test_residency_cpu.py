@@ -428,3 +428,36 @@ def test_gate_promote_consensus_fail_safe():
     assert all(run_ranks(_gate_tp, 3, -1, 2))                   # nothing new on one rank still replays together
     from vllm_moet_b200.residency import gate_promote_consensus
     assert gate_promote_consensus(lambda: 2) and not gate_promote_consensus(lambda: 0)
+
+
+def _replay_pp_stage(rank, world, fault_stage, base_dir):
+    """Pipeline stages with their own layers' caches: stage 0's experts are resident,
+    stage 1 misses.  Both stages replay the step together (and, with an injected read
+    fault on one stage, both refuse to replay)."""
+    import torch.distributed as dist
+    st = make_store("pack", L, E, SB, dir=os.path.join(base_dir, f"stage{rank}"), ckpt_id="pp")
+    fill(st)
+    c = ExpertCache(st, L, E, SB, 12, device="cpu", manager=False)
+    routes = [torch.tensor([0, 1]), torch.tensor([2]), torch.tensor([3])]
+    if rank == 0:
+        c.promote([(0, 0), (0, 1), (1, 2), (2, 3)])     # everything this stage routes is resident
+        c.step_end()
+    if rank == fault_stage:
+        st.inject_read_faults(1)
+    m = FakeModel(c, routes)
+    r = ReplayEngine(c, pp_group=dist.group.WORLD, fp_max=4, comm_device="cpu")
+    try:
+        n = r.run(m.step, m.restore, lambda: routes)
+        out = ("ok", n, len(m.outputs))
+    except FetchError:
+        out = ("refused", 0, len(m.outputs))
+    finally:
+        st.release()
+    return out
+
+
+def test_replay_pp_whole_pipeline_consensus(tmp_path):
+    res = run_ranks(_replay_pp_stage, 2, -1, str(tmp_path / "a"))
+    assert res[0] == res[1] == ("ok", 1, 2)           # stage 0 had no miss but replays with stage 1
+    res = run_ranks(_replay_pp_stage, 2, 1, str(tmp_path / "b"))
+    assert res[0][0] == res[1][0] == "refused"         # a failed read on stage 1: nobody replays

@@ -265,7 +265,8 @@ class LLM:
                              "(one decode step's routed experts); raise it or set VLLM_MOE_W2_FORCE_POOL=1")
         self.cache = build_expert_cache(self.mw, slots, kind, self.device, **kw)
         self.runner.attach_expert_cache(self.cache)
-        self.replay = ReplayEngine(self.cache, tp_group=tp_group, mode=m.replay_mode, fp_max=m.fp_max,
+        self.replay = ReplayEngine(self.cache, tp_group=tp_group, pp_group=self._pp_group, mode=m.replay_mode,
+                                   fp_max=m.fp_max,
                                    miss_tol=m.base_miss_tol)
 
     # ------------------------------------------------------------------ API

@@ -44,10 +44,16 @@ def _tp_reduce(t: torch.Tensor, group, op) -> torch.Tensor:
 
 
 class ReplayEngine:
+    """With ``pp_group`` (pipeline stages, each with its own layers' cache) the miss
+    count and the fetch outcome are also agreed over the pipeline, so every stage
+    replays the step together (its sends and receives pair up); the missing-expert
+    bitmap stays per stage (reference: PP base segment replay, M5 / M9)."""
+
     def __init__(self, cache: ExpertCache, tp_group=None, mode: str = "strict", fp_max: int = 32,
-                 miss_tol: int = 0, comm_device=None):
+                 miss_tol: int = 0, comm_device=None, pp_group=None):
         if mode not in ("strict", "approximate"):
             raise ValueError(mode)
+        self.pp_group = pp_group
         self.cache, self.group, self.mode = cache, tp_group, mode
         self.fp_max, self.miss_tol = fp_max, miss_tol
         self.comm_device = comm_device or cache.dev
@@ -71,9 +77,10 @@ class ReplayEngine:
 
     def read_misses(self) -> int:
         m = self.cache.miss_count.clone()
-        if self.group is not None:
-            import torch.distributed as dist
-            m = _tp_reduce(m.to(self.comm_device), self.group, dist.ReduceOp.MAX)
+        import torch.distributed as dist
+        for g in (self.group, self.pp_group):
+            if g is not None:
+                m = _tp_reduce(m.to(self.comm_device), g, dist.ReduceOp.MAX)
         return int(m.item())
 
     def fetch_consensus(self, pairs) -> None:
@@ -82,10 +89,13 @@ class ReplayEngine:
             self.cache.promote(pairs)
         except FetchError:
             ok = 0
-        if self.group is not None:
+        if self.group is not None or self.pp_group is not None:
             import torch.distributed as dist
             t = torch.tensor([ok], dtype=torch.int32, device=self.comm_device)
-            ok = int(_tp_reduce(t, self.group, dist.ReduceOp.MIN).item())
+            for g in (self.group, self.pp_group):
+                if g is not None:
+                    t = _tp_reduce(t, g, dist.ReduceOp.MIN)
+            ok = int(t.item())
         if not ok:
             self.stats["fetch_failed"] += 1
             raise FetchError("expert fetch failed on at least one rank (fail closed)")
