@@ -86,3 +86,50 @@ def test_delta_trace_counts():
     snap = t.snapshot(d)
     assert snap["hit_rate_distinct"] == 0.5 and snap["hit_rate_tokens"] == 5 / 8
     assert snap["coverage"] == 2 / 8 and snap["fp4_per_layer"] == [1, 1] and len(lines) == 1
+
+
+def _stop_prompt():
+    g = torch.Generator().manual_seed(5)
+    return torch.randint(3, 259, (12,), generator=g).tolist()
+
+
+def test_stop_strings_min_tokens_and_stop_ids():
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+    p = _stop_prompt()
+    full = llm.generate([p], SamplingParams(max_tokens=16, ignore_eos=True))[0].outputs[0]
+    stop = full.text[-2:]
+    i = full.text.find(stop)
+    cut = llm.generate([p], SamplingParams(max_tokens=16, ignore_eos=True, stop=[stop]))[0].outputs[0]
+    assert cut.finish_reason == "stop" and cut.stop_reason == stop and cut.text == full.text[:i]
+    assert cut.token_ids == full.token_ids[:len(cut.token_ids)] and len(cut.token_ids) <= len(full.token_ids)
+    inc = llm.generate([p], SamplingParams(max_tokens=16, ignore_eos=True, stop=stop,
+                                           include_stop_str_in_output=True))[0].outputs[0]
+    assert inc.text == full.text[:i + len(stop)]
+    # stop token ids apply even with ignore_eos (only EOS is ignored)
+    sid = full.token_ids[2]
+    k = full.token_ids.index(sid)
+    o = llm.generate([p], SamplingParams(max_tokens=16, ignore_eos=True, stop_token_ids=[sid]))[0].outputs[0]
+    assert o.finish_reason == "stop" and o.stop_reason == sid and o.token_ids == full.token_ids[:k + 1]
+    # min_tokens: no stop condition before it
+    first = full.token_ids[0]
+    o = llm.generate([p], SamplingParams(max_tokens=16, ignore_eos=True, stop_token_ids=[first],
+                                         min_tokens=4))[0].outputs[0]
+    assert len(o.token_ids) >= 4 and o.token_ids == full.token_ids[:len(o.token_ids)]
+    with pytest.raises(ValueError):
+        SamplingParams(max_tokens=2, min_tokens=3)
+
+
+def test_stop_stream_holds_back_partial_stops():
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.tokenizer import ByteTokenizer
+    from vllm_moet_b200.entrypoints.openai_server import _StopStream
+    tok = ByteTokenizer(1024)
+    ids = [ord(c) + 3 for c in "hello wor" "ld<END>tail"]
+    ss = _StopStream(tok, SamplingParams(max_tokens=64, stop=["<END>"]))
+    out = "".join(ss.push([t], False) for t in ids)
+    assert out == "hello world" and ss.done
+    ss = _StopStream(tok, SamplingParams(max_tokens=64, stop=["<END>"]))
+    out = "".join(ss.push([t], i == 6) for i, t in enumerate(ids[:7]))
+    assert out == "hello w"                    # finished without a stop: everything held back is flushed

@@ -137,3 +137,18 @@ def test_tp2_serving_followers_match_single_rank():
     one = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=128)
     want = one.generate([[5, 6, 7, 8]], SamplingParams(max_tokens=6, ignore_eos=True))[0].outputs[0].token_ids
     assert ids == want
+
+
+def test_stop_strings_over_http(server):
+    url, _ = server
+    g = __import__("torch").Generator().manual_seed(5)
+    p = __import__("torch").randint(3, 259, (12,), generator=g).tolist()
+    body = {"prompt": p, "max_tokens": 16, "ignore_eos": True}
+    full = requests.post(url + "/v1/completions", json=body, timeout=120).json()["choices"][0]["text"]
+    stop = full[-2:]
+    want = full[: full.find(stop)]
+    r = requests.post(url + "/v1/completions", json=dict(body, stop=stop), timeout=120).json()["choices"][0]
+    assert r["text"] == want and r["finish_reason"] == "stop" and r["stop_reason"] == stop
+    s = requests.post(url + "/v1/completions", json=dict(body, stop=[stop], stream=True), stream=True, timeout=120)
+    events = [ln[6:] for ln in s.iter_lines(decode_unicode=True) if ln.startswith("data: ")]
+    assert "".join(json.loads(e)["choices"][0]["text"] for e in events[:-1]) == want

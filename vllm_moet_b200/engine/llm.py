@@ -22,7 +22,7 @@ import torch
 from ..config import EngineConfig, ModelConfig, MoetConfig, ParallelConfig, get_preset
 from ..models.weights import ModelWeights, random_weights
 from .kv_manager import BlockManager
-from .sampling_params import CompletionOutput, RequestOutput, SamplingParams
+from .sampling_params import CompletionOutput, RequestOutput, SamplingParams, cut_at_stop
 from .tokenizer import ByteTokenizer
 
 
@@ -38,6 +38,8 @@ class _Req:
     t_first: float = 0.0
     t_done: float = 0.0
     callback: Optional[object] = None     # callback(new_token_ids, finish_reason) for streaming
+    text: Optional[str] = None            # final text when a stop string cut it
+    stop_reason: Optional[object] = None
 
 
 class LLM:
@@ -310,22 +312,32 @@ class LLM:
             self._run_native(reqs)
         else:
             self._run_torch(reqs)
-        return [RequestOutput(r.rid, r.prompt, [CompletionOutput(0, self.tokenizer.decode(r.out), r.out,
-                                                                 r.finish)],
+        return [RequestOutput(r.rid, r.prompt, [CompletionOutput(0, r.text if r.text is not None
+                                                                 else self.tokenizer.decode(r.out), r.out,
+                                                                 r.finish, r.stop_reason)],
                               metrics=dict(ttft_s=r.t_first - r.t_arrive, e2e_s=r.t_done - r.t_arrive))
                 for r in reqs]
 
     # ------------------------------------------------------------------ helpers
     def _emit(self, r: _Req, tokens) -> bool:
         n0 = len(r.out)
+        p = r.params
         for t in tokens:
             if r.finish:
                 break
             t = int(t)
             r.out.append(t)
-            if not r.params.ignore_eos and (t in r.params.stop_token_ids or t == self.tokenizer.eos_token_id):
-                r.finish = "stop"
-            elif len(r.out) >= r.params.max_tokens:
+            if len(r.out) >= p.min_tokens:
+                if t in p.stop_token_ids:
+                    r.finish, r.stop_reason = "stop", t
+                elif not p.ignore_eos and t == self.tokenizer.eos_token_id:
+                    r.finish = "stop"
+                elif p.stop:
+                    text = self.tokenizer.decode(r.out)
+                    cut, hit = cut_at_stop(text, p.stop, p.include_stop_str_in_output)
+                    if hit is not None:
+                        r.finish, r.stop_reason, r.text = "stop", hit, cut
+            if not r.finish and len(r.out) >= p.max_tokens:
                 r.finish = "length"
         if r.finish and not r.t_done:
             r.t_done = time.perf_counter()

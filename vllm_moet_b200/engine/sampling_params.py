@@ -13,15 +13,42 @@ class SamplingParams:
     top_k: int = 0
     seed: Optional[int] = None
     stop_token_ids: List[int] = field(default_factory=list)
-    ignore_eos: bool = False
+    ignore_eos: bool = False        # ignore the EOS token only; stop_token_ids and stop still apply
+    stop: List[str] = field(default_factory=list)        # stop strings (output text is cut before them)
+    include_stop_str_in_output: bool = False
+    min_tokens: int = 0             # no stop condition before this many tokens
 
     def __post_init__(self):
+        if isinstance(self.stop, str):
+            self.stop = [self.stop]
+        self.stop = [x for x in self.stop if x]
         if self.max_tokens < 1:
             raise ValueError("max_tokens must be >= 1")
+        if not 0 <= self.min_tokens <= self.max_tokens:
+            raise ValueError("min_tokens must be in [0, max_tokens]")
         if self.temperature < 0:
             raise ValueError("temperature must be >= 0")
         if not 0 < self.top_p <= 1:
             raise ValueError("top_p must be in (0, 1]")
+
+
+def find_stop(text: str, stops: List[str], start: int = 0):
+    """-> (index, stop string) of the earliest stop string in text[start:], or None."""
+    best = None
+    for s in stops:
+        i = text.find(s, start)
+        if i >= 0 and (best is None or i < best[0]):
+            best = (i, s)
+    return best
+
+
+def cut_at_stop(text: str, stops: List[str], include: bool = False):
+    """-> (text up to the first stop string, the stop string or None)."""
+    hit = find_stop(text, stops)
+    if hit is None:
+        return text, None
+    i, s = hit
+    return text[: i + (len(s) if include else 0)], s
 
 
 @dataclass
@@ -30,6 +57,7 @@ class CompletionOutput:
     text: str
     token_ids: List[int]
     finish_reason: Optional[str] = None
+    stop_reason: Optional[object] = None      # the stop token id or stop string that ended the request
 
 
 @dataclass

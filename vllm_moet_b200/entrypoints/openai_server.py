@@ -27,7 +27,7 @@ import time
 import uuid
 from typing import Any, Dict, List, Optional
 
-from ..engine.sampling_params import SamplingParams
+from ..engine.sampling_params import SamplingParams, cut_at_stop
 from . import chat_encoding
 
 
@@ -104,8 +104,37 @@ def _params_from(body: Dict[str, Any], default_max: int = 16) -> SamplingParams:
     if temp != 0.0:
         raise ValueError("only greedy decoding (temperature 0) is served on the MTP path")
     stop_ids = list(body.get("stop_token_ids") or [])
+    stop = body.get("stop") or []
     return SamplingParams(max_tokens=int(body.get("max_tokens") or body.get("max_completion_tokens") or default_max),
-                          temperature=0.0, stop_token_ids=stop_ids, ignore_eos=bool(body.get("ignore_eos", False)))
+                          temperature=0.0, stop_token_ids=stop_ids, ignore_eos=bool(body.get("ignore_eos", False)),
+                          stop=[stop] if isinstance(stop, str) else list(stop),
+                          include_stop_str_in_output=bool(body.get("include_stop_str_in_output", False)),
+                          min_tokens=int(body.get("min_tokens") or 0))
+
+
+class _StopStream:
+    """Incremental text for streaming with stop strings: a tail that could still be the
+    start of a stop string is held back until it is resolved (as vLLM streams)."""
+
+    def __init__(self, tok, params: SamplingParams):
+        self.tok, self.p = tok, params
+        self.ids, self.sent = [], 0
+        self.hold = max((len(x) for x in params.stop), default=1) - 1
+        self.done = False
+
+    def push(self, new_ids, finished: bool) -> str:
+        if self.done:
+            return ""
+        self.ids += list(new_ids)
+        text = self.tok.decode(self.ids)
+        cut, hit = cut_at_stop(text, self.p.stop, self.p.include_stop_str_in_output)
+        if hit is not None or finished:
+            self.done = True
+            out, self.sent = cut[self.sent:], len(cut)
+            return out
+        upto = max(self.sent, len(text) - self.hold)
+        out, self.sent = text[self.sent:upto], upto
+        return out
 
 
 def build_app(worker: EngineWorker):
@@ -175,13 +204,15 @@ def build_app(worker: EngineWorker):
 
             async def gen():
                 finish = None
+                ss = _StopStream(tok, params)
                 while finish is None:
                     ids, finish = await aq.get()
                     if finish and finish.startswith("error:"):
                         yield f"data: {json.dumps({'error': finish[6:]})}\n\n"
                         break
+                    text = ss.push(ids, finish is not None) if params.stop else tok.decode(ids)
                     chunk = {"id": rid, "object": "text_completion", "created": created, "model": name,
-                             "choices": [{"index": 0, "text": tok.decode(ids), "token_ids": ids,
+                             "choices": [{"index": 0, "text": text, "token_ids": ids,
                                           "finish_reason": finish}]}
                     yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
@@ -191,8 +222,9 @@ def build_app(worker: EngineWorker):
         for i, aq in enumerate(qs):
             ids, finish = await collect(aq)
             n_out += len(ids)
-            choices.append({"index": i, "text": tok.decode(ids), "token_ids": ids, "finish_reason": finish,
-                            "logprobs": None})
+            text, hit = cut_at_stop(tok.decode(ids), params.stop, params.include_stop_str_in_output)
+            choices.append({"index": i, "text": text, "token_ids": ids, "finish_reason": finish,
+                            "stop_reason": hit, "logprobs": None})
         return JSONResponse({"id": rid, "object": "text_completion", "created": created, "model": name,
                              "choices": choices,
                              "usage": {"prompt_tokens": sum(map(len, plist)), "completion_tokens": n_out,
@@ -214,9 +246,10 @@ def build_app(worker: EngineWorker):
             async def gen():
                 finish = None
                 first = True
+                ss = _StopStream(tok, params)
                 while finish is None:
                     ids, finish = await aq.get()
-                    delta = {"content": tok.decode(ids)}
+                    delta = {"content": ss.push(ids, finish is not None) if params.stop else tok.decode(ids)}
                     if first:
                         delta["role"] = "assistant"
                         first = False
@@ -226,7 +259,7 @@ def build_app(worker: EngineWorker):
                 yield "data: [DONE]\n\n"
             return StreamingResponse(gen(), media_type="text/event-stream")
         ids, finish = await collect(aq)
-        out_text = tok.decode(ids)
+        out_text = cut_at_stop(tok.decode(ids), params.stop, params.include_stop_str_in_output)[0]
         try:
             msg = chat_encoding.parse_completion(out_text, thinking=thinking)
         except ValueError:
