@@ -100,7 +100,11 @@ def test_streaming_and_chat(server):
     r = requests.post(url + "/v1/chat/completions", json={"messages": [{"role": "user", "content": "hello"}],
                                                           "max_tokens": 4, "ignore_eos": True}, timeout=120)
     assert r.ok and r.json()["choices"][0]["message"]["role"] == "assistant"
-    assert requests.post(url + "/v1/completions", json={"prompt": "x", "temperature": 0.7}).status_code == 400
+    assert requests.post(url + "/v1/completions", json={"prompt": "x", "temperature": -1}).status_code == 400
+    body = {"prompt": [5, 6, 7, 8], "max_tokens": 6, "ignore_eos": True, "temperature": 0.8, "seed": 3}
+    a = requests.post(url + "/v1/completions", json=body, timeout=120).json()["choices"][0]["token_ids"]
+    b = requests.post(url + "/v1/completions", json=body, timeout=120).json()["choices"][0]["token_ids"]
+    assert a == b and len(a) == 6                     # seeded sampling is reproducible
 
 
 def _tp_serving(rank, world):

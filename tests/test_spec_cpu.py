@@ -1,5 +1,7 @@
 """DSpark width scheduler (the reference's scheduler test semantics), the
 DSpark block drafter, and the greedy / stochastic rejection samplers."""
+import math
+
 import torch
 
 from vllm_moet_b200.spec import DSparkDrafter, allocate_widths, greedy_accept, rejection_sample
@@ -81,3 +83,57 @@ def test_quant_study_orders_formats():
     from vllm_moet_b200.tools.quant_study import study
     r = study(torch.randn(64, 256) * 0.02)
     assert r["nvfp4"][0] < r["2-bit codebook (auto)"][0] and r["mxfp4 (delta tier)"][0] < r["2-bit codebook (auto)"][0]
+
+
+def test_filter_probs_top_k_top_p():
+    from vllm_moet_b200.spec.rejection import filter_probs
+    logits = torch.tensor([[4.0, 3.0, 2.0, 1.0, 0.0]])
+    p = filter_probs(logits, 1.0, top_k=2)
+    assert (p[0, 2:] == 0).all() and abs(float(p.sum()) - 1) < 1e-6
+    full = torch.softmax(logits, -1)[0]
+    p = filter_probs(logits, 1.0, top_p=float(full[0] + full[1]) - 1e-4)      # needs the top two
+    assert (p[0, :2] > 0).all() and (p[0, 2:] == 0).all()
+    p = filter_probs(logits, 1.0, top_p=0.01)                                  # always keeps the top token
+    assert float(p[0, 0]) == 1.0
+    cold = filter_probs(logits, 1e-3)
+    assert float(cold[0, 0]) > 0.999
+
+
+def test_engine_sampling_top1_equals_greedy_and_seeds_reproduce():
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+    prompts = [[5, 6, 7, 8, 9], [40, 41, 42]]
+    greedy = [o.outputs[0].token_ids for o in llm.generate(prompts, SamplingParams(max_tokens=10, ignore_eos=True))]
+    top1 = [o.outputs[0].token_ids for o in llm.generate(prompts, SamplingParams(max_tokens=10, ignore_eos=True,
+                                                                                 temperature=0.9, top_k=1))]
+    assert top1 == greedy                     # the whole sampling path (prefill, rejection, bonus) at top-1
+    sp = SamplingParams(max_tokens=10, ignore_eos=True, temperature=1.5, seed=11)
+    a = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
+    b = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
+    c = [o.outputs[0].token_ids for o in llm.generate(prompts, SamplingParams(max_tokens=10, ignore_eos=True,
+                                                                              temperature=1.5, seed=12))]
+    assert a == b and a != c and a != greedy
+
+
+def test_engine_first_token_distribution():
+    """The first sampled token follows softmax(logits / T) of the reference model."""
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    from vllm_moet_b200.models import reference
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=0, max_model_len=64)
+    p = [5, 6, 7, 8, 9]
+    T = 0.02
+    lg, _ = reference.forward(llm.mw, torch.tensor(p), torch.arange(len(p)), reference.rope_cos_sin(llm.cfg, 64))
+    want = torch.softmax(lg[-1] / T, -1)
+    top = torch.topk(want, 3)
+    n = 300
+    counts = torch.zeros_like(want)
+    outs = llm.generate([p] * n, [SamplingParams(max_tokens=1, ignore_eos=True, temperature=T, seed=s)
+                                  for s in range(n)])
+    for o in outs:
+        counts[o.outputs[0].token_ids[0]] += 1
+    freq = counts / n
+    for i in top.indices.tolist():
+        sd = math.sqrt(float(want[i]) * (1 - float(want[i])) / n) + 1e-3
+        assert abs(float(freq[i]) - float(want[i])) < 5 * sd, (i, float(freq[i]), float(want[i]))

@@ -292,7 +292,7 @@ class LLM:
 
     def generate(self, prompts, sampling_params: Union[SamplingParams, Sequence[SamplingParams], None] = None,
                  use_tqdm: bool = False, callbacks: Optional[Sequence] = None) -> List[RequestOutput]:
-        """Greedy generation for a batch of prompts (str, token-id lists or
+        """Generation for a batch of prompts (str, token-id lists or
         {"prompt_token_ids": [...]}).  `callbacks[i](new_ids, finish_reason)` is
         called as tokens of prompt i are emitted (streaming)."""
         toks = self._normalize(prompts)
@@ -302,8 +302,9 @@ class LLM:
             sampling_params = [sampling_params] * len(toks)
         reqs = []
         for t, sp in zip(toks, sampling_params):
-            if sp.temperature != 0:
-                raise NotImplementedError("this engine serves greedy decoding (temperature 0) on the MTP path")
+            if sp.temperature != 0 and self.device.type == "cuda":
+                raise NotImplementedError("temperature > 0: the GPU runner verifies drafts greedily inside the "
+                                          "decode graph; sampling is served by the CPU engine")
             if len(t) + sp.max_tokens + self.k + 1 > self.ecfg.max_model_len:
                 raise ValueError(f"prompt ({len(t)}) + max_tokens ({sp.max_tokens}) exceeds max_model_len")
             reqs.append(_Req(f"req-{next(self._ids)}", t, sp, t_arrive=time.perf_counter(),
@@ -356,7 +357,7 @@ class LLM:
             while waiting and free:
                 r = waiting.popleft(); r.row = free.pop(0); rows[r.row] = r; adm.append(r)
             if adm:
-                firsts = self.runner.prefill([r.prompt for r in adm], [r.row for r in adm])
+                firsts = self.runner.prefill([r.prompt for r in adm], [r.row for r in adm], [r.params for r in adm])
                 for r, f in zip(adm, firsts):
                     r.t_first = time.perf_counter()
                     if self._emit(r, [f]):

@@ -42,23 +42,38 @@ class TorchRunner:
                        self.dcp_interleave)
 
     @torch.no_grad()
-    def prefill(self, prompts, rows):
+    def prefill(self, prompts, rows, params=None):
+        """params[i] (SamplingParams or None): temperature > 0 samples (per-row seeded
+        generator); the verify steps then use speculative rejection sampling."""
         with self._ctx():
-            return self._prefill(prompts, rows)
+            return self._prefill(prompts, rows, params or [None] * len(prompts))
 
-    def _prefill(self, prompts, rows):
+    def _sample_state(self, sp):
+        if sp is None or sp.temperature <= 0:
+            return None
+        g = torch.Generator(device=self.dev)
+        g.manual_seed(sp.seed if sp.seed is not None else int(torch.randint(0, 2**62, (1,))))
+        return dict(sp=sp, gen=g)
+
+    def _prefill(self, prompts, rows, params):
         firsts = []
-        for prompt, r in zip(prompts, rows):
+        for prompt, r, sp in zip(prompts, rows, params):
+            smp = self._sample_state(sp)
             n = len(prompt)
             main, mtp = self._kv(len(self.mw.layers)), self._kv(1)
             toks = torch.tensor(prompt, device=self.dev)
             if self.sp_group is not None:
                 from ..parallel.context import sp_prefill_forward
                 last, hid = sp_prefill_forward(self.mw, toks, self.cs, self.sp_group, main)
-                tgt = int(last.argmax())
             else:
                 logits, hid = ref.forward(self.mw, toks, torch.arange(n, device=self.dev), self.cs, main)
-                tgt = int(logits[-1].argmax())
+                last = logits[-1]
+            if smp is None:
+                tgt = int(last.argmax())
+            else:
+                from ..spec.rejection import filter_probs
+                p = filter_probs(last[None], smp["sp"].temperature, smp["sp"].top_k, smp["sp"].top_p)
+                tgt = int(torch.multinomial(p[0], 1, generator=smp["gen"]))
             drafts = []
             if self.k:
                 nxt = torch.tensor(prompt[1:] + [tgt], device=self.dev)
@@ -69,7 +84,7 @@ class TorchRunner:
                     ml, h = ref.mtp_forward(self.mw, h, torch.tensor([d], device=self.dev),
                                             torch.tensor([n + j - 1], device=self.dev), self.cs, mtp)
                     d = int(ml[-1].argmax()); drafts.append(d)
-            self.rows[r] = dict(main=main, mtp=mtp, tokens=[tgt] + drafts, pos=n)
+            self.rows[r] = dict(main=main, mtp=mtp, tokens=[tgt] + drafts, pos=n, sample=smp)
             firsts.append(tgt)
         return firsts
 
@@ -89,10 +104,21 @@ class TorchRunner:
             toks = torch.tensor(st["tokens"], device=self.dev)
             pos = torch.arange(p, p + k + 1, device=self.dev)
             logits, hid = ref.forward(self.mw, toks, pos, self.cs, st["main"])
-            tg = logits.argmax(-1).tolist()
-            a = 0
-            while a < k and st["tokens"][a + 1] == tg[a]:
-                a += 1
+            smp = st.get("sample")
+            if smp is None:
+                tg = logits.argmax(-1).tolist()
+                a = 0
+                while a < k and st["tokens"][a + 1] == tg[a]:
+                    a += 1
+            else:       # speculative sampling: the MTP drafts are greedy, so q is one-hot
+                from ..spec.rejection import filter_probs, rejection_sample
+                sp = smp["sp"]
+                probs = filter_probs(logits, sp.temperature, sp.top_k, sp.top_p)      # [k+1, V]
+                d = toks[1:].long()
+                q = torch.nn.functional.one_hot(d, probs.shape[-1]).float()
+                n_acc, em = rejection_sample(probs[None], q[None], d[None], generator=smp["gen"])
+                a = int(n_acc[0])
+                tg = em[0, : a + 1].tolist() + [int(em[0, a])] * (k - a)   # MTP input: accepted + sampled
             emitted = tg[: a + 1]
             drafts = []
             if k:

@@ -101,12 +101,15 @@ def follower_loop(llm, tp_group):
 
 def _params_from(body: Dict[str, Any], default_max: int = 16) -> SamplingParams:
     temp = float(body.get("temperature", 0.0) or 0.0)
-    if temp != 0.0:
-        raise ValueError("only greedy decoding (temperature 0) is served on the MTP path")
+    if temp < 0:
+        raise ValueError("temperature must be >= 0")
     stop_ids = list(body.get("stop_token_ids") or [])
     stop = body.get("stop") or []
+    seed = body.get("seed")
     return SamplingParams(max_tokens=int(body.get("max_tokens") or body.get("max_completion_tokens") or default_max),
-                          temperature=0.0, stop_token_ids=stop_ids, ignore_eos=bool(body.get("ignore_eos", False)),
+                          temperature=temp, top_p=float(body.get("top_p", 1.0) or 1.0),
+                          top_k=int(body.get("top_k") or 0), seed=None if seed is None else int(seed),
+                          stop_token_ids=stop_ids, ignore_eos=bool(body.get("ignore_eos", False)),
                           stop=[stop] if isinstance(stop, str) else list(stop),
                           include_stop_str_in_output=bool(body.get("include_stop_str_in_output", False)),
                           min_tokens=int(body.get("min_tokens") or 0))
@@ -178,6 +181,10 @@ def build_app(worker: EngineWorker):
         lines = [f"moet_{k}_total {v}" for k, v in worker.stats.items()]
         return PlainTextResponse("\n".join(lines) + "\n")
 
+    def _servable(params):
+        if params.temperature > 0 and worker.llm.device.type == "cuda":
+            raise HTTPException(400, "temperature > 0 is served by the CPU engine; the GPU runner decodes greedily")
+
     def _prompt_ids(p):
         if isinstance(p, str):
             return [tok.bos_token_id] + tok.encode(p)
@@ -191,6 +198,7 @@ def build_app(worker: EngineWorker):
             params = _params_from(body)
         except ValueError as e:
             raise HTTPException(400, str(e))
+        _servable(params)
         prompts = body.get("prompt")
         if isinstance(prompts, list) and prompts and not isinstance(prompts[0], int):
             plist = [_prompt_ids(p) for p in prompts]
@@ -236,6 +244,7 @@ def build_app(worker: EngineWorker):
             params = _params_from(body)
         except ValueError as e:
             raise HTTPException(400, str(e))
+        _servable(params)
         effort = body.get("reasoning_effort", "none")
         text = chat_encoding.render(body.get("messages", []), tools=body.get("tools"), reasoning_effort=effort)
         prompt = [tok.bos_token_id] + tok.encode(text)

@@ -11,6 +11,8 @@
   first rejection the token is resampled from normalize(max(p - q, 0)); if all
   drafts pass, a bonus token is sampled from p at the next position.  The
   output distribution equals sampling from p token by token.
+* :func:`filter_probs` -- temperature, top-k and nucleus (top-p) filtering of
+  logits into the target distribution p.
 """
 from __future__ import annotations
 
@@ -59,3 +61,22 @@ def rejection_sample(target_probs: torch.Tensor, draft_probs: torch.Tensor, draf
             dist = target_probs[r, a]
         emitted[r, a] = torch.multinomial(dist, 1, generator=generator)[0]
     return n_acc, emitted
+
+
+def filter_probs(logits: torch.Tensor, temperature: float, top_k: int = 0, top_p: float = 1.0) -> torch.Tensor:
+    """logits [R, V] -> probabilities [R, V]: softmax(logits / T) restricted to the top_k
+    tokens (0 = all) and to the smallest set whose probability reaches top_p (at least one)."""
+    x = logits.float() / max(temperature, 1e-6)
+    if top_k and 0 < top_k < x.shape[-1]:
+        kth = torch.topk(x, top_k, dim=-1).values[..., -1:]
+        x = x.masked_fill(x < kth, float("-inf"))
+    p = torch.softmax(x, dim=-1)
+    if top_p < 1.0:
+        sp, idx = torch.sort(p, dim=-1, descending=True)
+        before = torch.cumsum(sp, dim=-1) - sp            # mass strictly above each token
+        keep = before < top_p
+        keep[..., 0] = True
+        mask = torch.zeros_like(p, dtype=torch.bool).scatter(-1, idx, keep)
+        p = torch.where(mask, p, torch.zeros_like(p))
+        p = p / p.sum(dim=-1, keepdim=True)
+    return p
