@@ -124,7 +124,7 @@ def test_router_results_spread_and_streaming(dp_cluster):
     m = requests.get(url + "/metrics").text
     assert "moet_requests_total" in m and "moet_router_requests_total" in m
     assert requests.get(url + "/health").json()["healthy_replicas"] == 2
-    assert requests.post(url + "/v1/completions", json={"prompt": "x", "temperature": 0.7}).status_code == 400
+    assert requests.post(url + "/v1/completions", json={"prompt": "x", "temperature": -1}).status_code == 400
 
 
 def test_router_fails_over_when_a_replica_stops(dp_cluster):
