@@ -133,3 +133,29 @@ def test_stop_stream_holds_back_partial_stops():
     ss = _StopStream(tok, SamplingParams(max_tokens=64, stop=["<END>"]))
     out = "".join(ss.push([t], i == 6) for i, t in enumerate(ids[:7]))
     assert out == "hello w"                    # finished without a stop: everything held back is flushed
+
+
+def test_logprobs_match_reference():
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+    p = [5, 6, 7, 8, 9, 10]
+    o = llm.generate([p], SamplingParams(max_tokens=7, ignore_eos=True, logprobs=3))[0].outputs[0]
+    assert len(o.logprobs) == len(o.token_ids) == 7
+    cs = reference.rope_cos_sin(llm.cfg, 64)
+    toks = list(p)
+    total = 0.0
+    for t, d in zip(o.token_ids, o.logprobs):
+        lg, _ = reference.forward(llm.mw, torch.tensor(toks), torch.arange(len(toks)), cs)
+        lp = torch.log_softmax(lg[-1], -1)
+        assert abs(d[t] - float(lp[t])) < 1e-4
+        top = torch.topk(lp, 3).indices.tolist()
+        assert set(top) <= set(d) and len(d) <= 4
+        total += d[t]
+        toks.append(t)
+    assert abs(o.cumulative_logprob - total) < 1e-6
+    got = []
+    llm.generate([p], SamplingParams(max_tokens=3, ignore_eos=True, logprobs=0),
+                 callbacks=[lambda ids, fin, lp=None: got.extend(lp or [])])
+    assert len(got) == 3 and all(len(d) == 1 for d in got)
+    assert llm.generate([p], SamplingParams(max_tokens=2))[0].outputs[0].logprobs is None

@@ -461,3 +461,29 @@ def test_replay_pp_whole_pipeline_consensus(tmp_path):
     assert res[0] == res[1] == ("ok", 1, 2)           # stage 0 had no miss but replays with stage 1
     res = run_ranks(_replay_pp_stage, 2, 1, str(tmp_path / "b"))
     assert res[0][0] == res[1][0] == "refused"         # a failed read on stage 1: nobody replays
+
+
+def test_gate_score_from_vocab_shards_is_exact():
+    g = torch.Generator().manual_seed(9)
+    logits = torch.randn(5, 101, generator=g) * 3
+    shards = torch.tensor_split(logits, 3, dim=1)
+    parts = torch.stack([ConfidenceGate.row_stats(s) for s in shards])
+    merged = ConfidenceGate.merge_stats(parts)
+    assert torch.allclose(merged, ConfidenceGate.row_stats(logits), atol=1e-5)
+    for sig in ("maxprob", "margin"):
+        gt = ConfidenceGate(signal=sig)
+        assert abs(gt.score_stats(merged) - gt.score(logits)) < 1e-6
+
+
+def _gate_score_tp(rank, world):
+    import torch.distributed as dist
+    g = torch.Generator().manual_seed(9)
+    logits = torch.randn(4, 64, generator=g) * 2
+    shard = torch.tensor_split(logits, world, dim=1)[rank]
+    gt = ConfidenceGate(signal="margin", agg="q0.5")
+    return gt.score(shard, tp_group=dist.group.WORLD), gt.score(logits)
+
+
+def test_gate_score_tp_ranks_agree():
+    res = run_ranks(_gate_score_tp, 3)
+    assert all(abs(a - b) < 1e-6 for a, b in res) and len({round(a, 9) for a, _ in res}) == 1

@@ -156,3 +156,19 @@ def test_stop_strings_over_http(server):
     s = requests.post(url + "/v1/completions", json=dict(body, stop=[stop], stream=True), stream=True, timeout=120)
     events = [ln[6:] for ln in s.iter_lines(decode_unicode=True) if ln.startswith("data: ")]
     assert "".join(json.loads(e)["choices"][0]["text"] for e in events[:-1]) == want
+
+
+def test_logprobs_over_http(server):
+    url, _ = server
+    r = requests.post(url + "/v1/completions", json={"prompt": [5, 6, 7, 8], "max_tokens": 4, "ignore_eos": True,
+                                                     "logprobs": 2}, timeout=120).json()["choices"][0]
+    lp = r["logprobs"]
+    assert len(lp["token_logprobs"]) == 4 and all(x <= 0 for x in lp["token_logprobs"])
+    assert len(lp["top_logprobs"]) == 4 and lp["text_offset"][0] == 0
+    c = requests.post(url + "/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}],
+                                                          "max_tokens": 3, "ignore_eos": True, "logprobs": True,
+                                                          "top_logprobs": 2}, timeout=120).json()["choices"][0]
+    content = c["logprobs"]["content"]
+    assert len(content) == 3 and all(len(e["top_logprobs"]) == 2 and e["logprob"] <= 0 for e in content)
+    plain = requests.post(url + "/v1/completions", json={"prompt": [5, 6], "max_tokens": 2}, timeout=120).json()
+    assert plain["choices"][0]["logprobs"] is None

@@ -233,8 +233,14 @@ class NativeRunner:
             self._moe_index = {id(lw): i for i, lw in enumerate(moe_layers(self.mw))}
 
     def main_logits(self, B: int):
-        """Logits [B*(1+k), V] of the last decode step of bucket B (verify rows)."""
-        return self._bucket_ws(B).bufs.get(("main.logits", torch.float32))
+        """Logits [B*(1+k), V] of the last decode step of bucket B (verify rows, row i*(k+1)+j);
+        None where this rank has no head (PP stages before the last).  V is this rank's
+        vocab shard under TP."""
+        b = self._bucket_ws(B).bufs.get(("main.logits", torch.float32))
+        if b is None or getattr(self.mw, "lm_head", None) is None:
+            return None
+        V = self.mw.lm_head.w.shape[0]
+        return b[: B * (self.k + 1) * V].view(B * (self.k + 1), V)
 
     def route_ids(self, B: int):
         """Per-MoE-layer routed expert ids of the last decode step of bucket B."""

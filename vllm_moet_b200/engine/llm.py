@@ -39,6 +39,7 @@ class _Req:
     t_done: float = 0.0
     callback: Optional[object] = None     # callback(new_token_ids, finish_reason) for streaming
     text: Optional[str] = None            # final text when a stop string cut it
+    logprobs: Optional[list] = None       # per emitted token {token: logprob} (when requested)
     stop_reason: Optional[object] = None
 
 
@@ -302,6 +303,8 @@ class LLM:
             sampling_params = [sampling_params] * len(toks)
         reqs = []
         for t, sp in zip(toks, sampling_params):
+            if sp.logprobs is not None and self.device.type == "cuda" and self._tp_group is not None:
+                raise NotImplementedError("logprobs under tensor parallelism: each rank holds a vocab shard")
             if sp.temperature != 0 and self.device.type == "cuda":
                 raise NotImplementedError("temperature > 0: the GPU runner verifies drafts greedily inside the "
                                           "decode graph; sampling is served by the CPU engine")
@@ -313,21 +316,31 @@ class LLM:
             self._run_native(reqs)
         else:
             self._run_torch(reqs)
-        return [RequestOutput(r.rid, r.prompt, [CompletionOutput(0, r.text if r.text is not None
-                                                                 else self.tokenizer.decode(r.out), r.out,
-                                                                 r.finish, r.stop_reason)],
+        return [RequestOutput(r.rid, r.prompt, [CompletionOutput(
+                    0, r.text if r.text is not None else self.tokenizer.decode(r.out), r.out, r.finish, r.stop_reason,
+                    r.logprobs, (sum(d[t] for d, t in zip(r.logprobs, r.out)) if r.logprobs is not None else None))],
                               metrics=dict(ttft_s=r.t_first - r.t_arrive, e2e_s=r.t_done - r.t_arrive))
                 for r in reqs]
 
     # ------------------------------------------------------------------ helpers
-    def _emit(self, r: _Req, tokens) -> bool:
+    def _emit(self, r: _Req, tokens, logits=None) -> bool:
+        """Append emitted tokens (stop conditions apply per token); `logits` [n, V] are the
+        rows that predicted them (for requested logprobs)."""
         n0 = len(r.out)
         p = r.params
-        for t in tokens:
+        entries = None
+        if p.logprobs is not None and logits is not None:
+            from .sampling_params import logprob_entries
+            entries = logprob_entries(logits[: len(tokens)], [int(t) for t in tokens], p.logprobs)
+            if r.logprobs is None:
+                r.logprobs = []
+        for j, t in enumerate(tokens):
             if r.finish:
                 break
             t = int(t)
             r.out.append(t)
+            if entries is not None:
+                r.logprobs.append(entries[j])
             if len(r.out) >= p.min_tokens:
                 if t in p.stop_token_ids:
                     r.finish, r.stop_reason = "stop", t
@@ -343,7 +356,10 @@ class LLM:
         if r.finish and not r.t_done:
             r.t_done = time.perf_counter()
         if r.callback is not None and (len(r.out) > n0 or r.finish):
-            r.callback(r.out[n0:], r.finish)
+            if p.logprobs is not None:
+                r.callback(r.out[n0:], r.finish, (r.logprobs or [])[n0:])
+            else:
+                r.callback(r.out[n0:], r.finish)
         return r.finish is not None
 
     def _run_torch(self, reqs):
@@ -360,7 +376,7 @@ class LLM:
                 firsts = self.runner.prefill([r.prompt for r in adm], [r.row for r in adm], [r.params for r in adm])
                 for r, f in zip(adm, firsts):
                     r.t_first = time.perf_counter()
-                    if self._emit(r, [f]):
+                    if self._emit(r, [f], self.runner.last_logits.get(r.row)):
                         rows[r.row] = None; self.runner.release(r.row)
             live = [i for i, r in enumerate(rows) if r is not None]
             if not live:
@@ -369,7 +385,7 @@ class LLM:
             steps += 1
             for i, (toks, a) in res.items():
                 accepted += a
-                if self._emit(rows[i], toks):
+                if self._emit(rows[i], toks, self.runner.last_logits.get(i)):
                     self.runner.release(i); rows[i] = None
         self.stats = dict(steps=steps, accepted=accepted)
 
@@ -415,9 +431,12 @@ class LLM:
                 with self.timers.span("prefill") if self.timers is not None else contextlib.nullcontext():
                     firsts = runner.prefill([r.prompt for r in adm], bts, [r.row for r in adm], st).tolist()
                 now = time.perf_counter()
-                for r, f in zip(adm, firsts):
+                want_lp = any(r.params.logprobs is not None for r in adm)
+                pl = runner.ws_prefill.get("main.logits", (len(adm), self.cfg.vocab), torch.float32) if want_lp \
+                    else None
+                for j, (r, f) in enumerate(zip(adm, firsts)):
                     r.t_first = now
-                    if self._emit(r, [f]):
+                    if self._emit(r, [f], pl[j:j + 1] if pl is not None else None):
                         self._finish_row(r, rows)
             live = [r is not None for r in rows]
             if not any(live):
@@ -455,12 +474,15 @@ class LLM:
             t_decode += time.perf_counter() - t0
             runner.check_status("decode step")
             steps += 1
+            dl = runner.main_logits(B) if any(r is not None and r.params.logprobs is not None for r in rows) \
+                else None
             for i, r in enumerate(rows):
                 if r is None:
                     continue
                 a = int(pin_acc[i])
                 accepted += a
-                if self._emit(r, pin_out[i, :a + 1].tolist()):
+                lg = dl[i * kp1: i * kp1 + a + 1] if dl is not None else None      # verify rows of this request
+                if self._emit(r, pin_out[i, :a + 1].tolist(), lg):
                     self._finish_row(r, rows)
         self.stats = dict(steps=steps, accepted=accepted, decode_s=t_decode, bucket=B)
 
@@ -489,12 +511,12 @@ class LLM:
                     step()
                 return logits[rows] if logits is not None else None     # no head before the last PP stage
             if self._pp_group is not None:
-                fired = self._pp_gate(B, run_step, lambda: self.gate.score(logits[rows]))
+                fired = self._pp_gate(B, run_step, lambda: self.gate.score(logits[rows], tp_group=self._tp_group))
                 self.delta.stats["gate_replays"] += fired
                 self.delta.step_end()
                 return
             # the step already ran once: score it, fire, replay (at most gate_fp_max times)
-            score = self.gate.score(logits[rows])
+            score = self.gate.score(logits[rows], tp_group=self._tp_group)
             score0, fired, iters = score, 0, []
             timing = self.ecfg.moet.gate_fire_timing
             while fired < self.gate.fp_max and self.gate.should_fire(score):
@@ -508,7 +530,7 @@ class LLM:
                 if timing:
                     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     e0.record()
-                score = self.gate.score(run_step())
+                score = self.gate.score(run_step(), tp_group=self._tp_group)
                 it = {"promoted": len(promote), "score": score}
                 if timing:
                     e1.record()
@@ -545,7 +567,7 @@ class LLM:
                                    device=self.device):
                 break
             out = run_step()
-            score = self.gate.score(out) if last else 0.0
+            score = self.gate.score(out, tp_group=self._tp_group) if last else 0.0
             fired += 1
         return fired
 

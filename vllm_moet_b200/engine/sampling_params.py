@@ -2,7 +2,7 @@
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from typing import List, Optional
+from typing import Dict, List, Optional
 
 
 @dataclass
@@ -17,6 +17,7 @@ class SamplingParams:
     stop: List[str] = field(default_factory=list)        # stop strings (output text is cut before them)
     include_stop_str_in_output: bool = False
     min_tokens: int = 0             # no stop condition before this many tokens
+    logprobs: Optional[int] = None  # per generated token: the chosen token's and the top-N log-probabilities
 
     def __post_init__(self):
         if isinstance(self.stop, str):
@@ -58,6 +59,8 @@ class CompletionOutput:
     token_ids: List[int]
     finish_reason: Optional[str] = None
     stop_reason: Optional[object] = None      # the stop token id or stop string that ended the request
+    logprobs: Optional[List[Dict[int, float]]] = None   # per token: {token id: log-probability}
+    cumulative_logprob: Optional[float] = None
 
 
 @dataclass
@@ -67,3 +70,24 @@ class RequestOutput:
     outputs: List[CompletionOutput]
     finished: bool = True
     metrics: dict = field(default_factory=dict)
+
+
+def logprob_entries(logits, tokens, top_n: int):
+    """logits [n, V] (the rows that predicted `tokens`) -> [{token: logprob}] with the chosen
+    token and the top_n alternatives of each row (raw model distribution, before sampling
+    filters)."""
+    import torch
+    lp = torch.log_softmax(logits.float(), dim=-1)
+    tok = torch.as_tensor(tokens, device=lp.device).long().view(-1, 1)
+    chosen = lp.gather(1, tok).squeeze(1).cpu().tolist()
+    out = []
+    if top_n and top_n > 0:
+        v, i = torch.topk(lp, min(top_n, lp.shape[-1]), dim=-1)
+        v, i = v.cpu().tolist(), i.cpu().tolist()
+    for r, t in enumerate(tok.view(-1).tolist()):
+        d = {int(t): float(chosen[r])}
+        if top_n and top_n > 0:
+            for tt, vv in zip(i[r], v[r]):
+                d.setdefault(int(tt), float(vv))
+        out.append(d)
+    return out

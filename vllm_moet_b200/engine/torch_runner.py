@@ -18,6 +18,7 @@ class TorchRunner:
         self.dev = torch.device(device)
         self.cs = ref.rope_cos_sin(mw.cfg, max_len + 64, self.dev)
         self.rows = {}
+        self.last_logits = {}           # row -> logits rows that predicted the tokens emitted by the last call
         self.tp_group = tp_group        # tensor-parallel CPU ranks (gloo): sharded weights, all-reduced partials
         self.sp_group = sp_group        # sequence-parallel prefill ranks: prompt chunks, gathered MLA latents
         self.dcp_group = dcp_group      # decode-context-parallel ranks: KV interleaved by position, LSE merge
@@ -68,6 +69,7 @@ class TorchRunner:
             else:
                 logits, hid = ref.forward(self.mw, toks, torch.arange(n, device=self.dev), self.cs, main)
                 last = logits[-1]
+            self.last_logits[r] = last[None]
             if smp is None:
                 tgt = int(last.argmax())
             else:
@@ -120,6 +122,7 @@ class TorchRunner:
                 a = int(n_acc[0])
                 tg = em[0, : a + 1].tolist() + [int(em[0, a])] * (k - a)   # MTP input: accepted + sampled
             emitted = tg[: a + 1]
+            self.last_logits[r] = logits[: a + 1]
             drafts = []
             if k:
                 st["mtp"].truncate(p)
@@ -138,3 +141,4 @@ class TorchRunner:
 
     def release(self, r):
         self.rows.pop(r, None)
+        self.last_logits.pop(r, None)

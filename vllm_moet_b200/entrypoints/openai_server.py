@@ -106,13 +106,18 @@ def _params_from(body: Dict[str, Any], default_max: int = 16) -> SamplingParams:
     stop_ids = list(body.get("stop_token_ids") or [])
     stop = body.get("stop") or []
     seed = body.get("seed")
+    lp = body.get("logprobs")
+    if isinstance(lp, bool):          # chat: logprobs true + top_logprobs n
+        lp = int(body.get("top_logprobs") or 0) if lp else None
+    elif lp is not None:
+        lp = int(lp)
     return SamplingParams(max_tokens=int(body.get("max_tokens") or body.get("max_completion_tokens") or default_max),
                           temperature=temp, top_p=float(body.get("top_p", 1.0) or 1.0),
                           top_k=int(body.get("top_k") or 0), seed=None if seed is None else int(seed),
                           stop_token_ids=stop_ids, ignore_eos=bool(body.get("ignore_eos", False)),
                           stop=[stop] if isinstance(stop, str) else list(stop),
                           include_stop_str_in_output=bool(body.get("include_stop_str_in_output", False)),
-                          min_tokens=int(body.get("min_tokens") or 0))
+                          min_tokens=int(body.get("min_tokens") or 0), logprobs=lp)
 
 
 class _StopStream:
@@ -153,19 +158,41 @@ def build_app(worker: EngineWorker):
         loop = asyncio.get_running_loop()
         aq: "asyncio.Queue" = asyncio.Queue()
 
-        def cb(ids, finish):
-            loop.call_soon_threadsafe(aq.put_nowait, (list(ids), finish))
+        def cb(ids, finish, lp=None):
+            loop.call_soon_threadsafe(aq.put_nowait, (list(ids), finish, lp))
         worker.submit(prompt_ids, params, cb)
         return aq
 
     async def collect(aq):
-        ids, finish = [], None
+        ids, finish, lps = [], None, []
         while finish is None:
-            new, finish = await aq.get()
+            new, finish, lp = await aq.get()
             ids += new
+            lps += lp or []
         if finish.startswith("error:"):
             raise HTTPException(500, finish[6:])
-        return ids, finish
+        return ids, finish, lps
+
+    def completion_logprobs(ids, lps):
+        """OpenAI completions format: tokens, token_logprobs, top_logprobs, text_offset."""
+        toks = [tok.decode([t]) for t in ids]
+        offs, o = [], 0
+        for t in toks:
+            offs.append(o)
+            o += len(t)
+        return {"tokens": toks, "token_logprobs": [d.get(t) for d, t in zip(lps, ids)],
+                "top_logprobs": [{tok.decode([k]): v for k, v in d.items()} for d in lps], "text_offset": offs}
+
+    def chat_logprobs(ids, lps, top_n):
+        """OpenAI chat format: content[] of {token, logprob, bytes, top_logprobs[]}."""
+        out = []
+        for t, d in zip(ids, lps):
+            s = tok.decode([t])
+            alts = sorted(d.items(), key=lambda kv: -kv[1])[:top_n]
+            out.append({"token": s, "logprob": d.get(t), "bytes": list(s.encode("utf-8")),
+                        "top_logprobs": [{"token": tok.decode([k]), "logprob": v,
+                                          "bytes": list(tok.decode([k]).encode("utf-8"))} for k, v in alts]})
+        return {"content": out}
 
     @app.get("/health")
     async def health():
@@ -214,13 +241,14 @@ def build_app(worker: EngineWorker):
                 finish = None
                 ss = _StopStream(tok, params)
                 while finish is None:
-                    ids, finish = await aq.get()
+                    ids, finish, lp = await aq.get()
                     if finish and finish.startswith("error:"):
                         yield f"data: {json.dumps({'error': finish[6:]})}\n\n"
                         break
                     text = ss.push(ids, finish is not None) if params.stop else tok.decode(ids)
                     chunk = {"id": rid, "object": "text_completion", "created": created, "model": name,
                              "choices": [{"index": 0, "text": text, "token_ids": ids,
+                                          "logprobs": completion_logprobs(ids, lp) if lp else None,
                                           "finish_reason": finish}]}
                     yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
@@ -228,11 +256,12 @@ def build_app(worker: EngineWorker):
         qs = [run_request(p, params) for p in plist]
         choices, n_out = [], 0
         for i, aq in enumerate(qs):
-            ids, finish = await collect(aq)
+            ids, finish, lps = await collect(aq)
             n_out += len(ids)
             text, hit = cut_at_stop(tok.decode(ids), params.stop, params.include_stop_str_in_output)
             choices.append({"index": i, "text": text, "token_ids": ids, "finish_reason": finish,
-                            "stop_reason": hit, "logprobs": None})
+                            "stop_reason": hit,
+                            "logprobs": completion_logprobs(ids, lps) if params.logprobs is not None else None})
         return JSONResponse({"id": rid, "object": "text_completion", "created": created, "model": name,
                              "choices": choices,
                              "usage": {"prompt_tokens": sum(map(len, plist)), "completion_tokens": n_out,
@@ -257,7 +286,7 @@ def build_app(worker: EngineWorker):
                 first = True
                 ss = _StopStream(tok, params)
                 while finish is None:
-                    ids, finish = await aq.get()
+                    ids, finish, _ = await aq.get()
                     delta = {"content": ss.push(ids, finish is not None) if params.stop else tok.decode(ids)}
                     if first:
                         delta["role"] = "assistant"
@@ -267,14 +296,16 @@ def build_app(worker: EngineWorker):
                     yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(gen(), media_type="text/event-stream")
-        ids, finish = await collect(aq)
+        ids, finish, lps = await collect(aq)
         out_text = cut_at_stop(tok.decode(ids), params.stop, params.include_stop_str_in_output)[0]
         try:
             msg = chat_encoding.parse_completion(out_text, thinking=thinking)
         except ValueError:
             msg = {"role": "assistant", "content": out_text}     # a free-form completion (random-init models)
         return JSONResponse({"id": rid, "object": "chat.completion", "created": created, "model": name,
-                             "choices": [{"index": 0, "message": msg, "finish_reason": finish}],
+                             "choices": [{"index": 0, "message": msg, "finish_reason": finish,
+                                          "logprobs": chat_logprobs(ids, lps, params.logprobs)
+                                          if params.logprobs is not None else None}],
                              "usage": {"prompt_tokens": len(prompt), "completion_tokens": len(ids),
                                        "total_tokens": len(prompt) + len(ids)}})
 

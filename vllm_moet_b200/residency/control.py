@@ -131,19 +131,42 @@ class ConfidenceGate:
         self.fp_max, self.max_promote = fp_max, max_promote
         self.stats = collections.Counter()
 
-    def score(self, logits: torch.Tensor, rows: Optional[torch.Tensor] = None) -> float:
-        """logits [R, V] (the verify rows).  maxprob = exp(top1 - lse); margin = p1 - p2."""
-        x = logits.float() if rows is None else logits[rows].float()
-        lse = torch.logsumexp(x, dim=-1)
-        if self.signal == "maxprob":
-            s = torch.exp(x.max(dim=-1).values - lse)
-        else:
-            top2 = x.topk(2, dim=-1).values
-            s = torch.exp(top2[:, 0] - lse) - torch.exp(top2[:, 1] - lse)
+    @staticmethod
+    def row_stats(logits: torch.Tensor) -> torch.Tensor:
+        """logits [R, V] (a full vocab or one rank's vocab shard) -> [R, 3] (top1, top2, lse)."""
+        x = logits.float()
+        top2 = x.topk(min(2, x.shape[-1]), dim=-1).values
+        if top2.shape[-1] < 2:
+            top2 = torch.cat([top2, torch.full_like(top2, float("-inf"))], dim=-1)
+        return torch.stack([top2[:, 0], top2[:, 1], torch.logsumexp(x, dim=-1)], dim=-1)
+
+    @staticmethod
+    def merge_stats(parts: torch.Tensor) -> torch.Tensor:
+        """[W, R, 3] per-shard stats -> [R, 3] of the whole vocab (exact: global top-2 from
+        every shard's top-2, log-sum-exp of the shards' log-sum-exps)."""
+        cand = parts[..., :2].permute(1, 0, 2).reshape(parts.shape[1], -1)   # [R, 2W]
+        top2 = cand.topk(2, dim=-1).values
+        return torch.stack([top2[:, 0], top2[:, 1], torch.logsumexp(parts[..., 2], dim=0)], dim=-1)
+
+    def score_stats(self, st: torch.Tensor) -> float:
+        t1, t2, lse = st[:, 0], st[:, 1], st[:, 2]
+        s = torch.exp(t1 - lse) if self.signal == "maxprob" else torch.exp(t1 - lse) - torch.exp(t2 - lse)
         if self.agg == "min":
             return float(s.min())
-        q = float(self.agg[1:])
-        return float(torch.quantile(s, q))
+        return float(torch.quantile(s, float(self.agg[1:])))
+
+    def score(self, logits: torch.Tensor, rows: Optional[torch.Tensor] = None, tp_group=None) -> float:
+        """logits [R, V] (the verify rows).  maxprob = exp(top1 - lse); margin = p1 - p2.
+        Under TP (vocab-sharded logits) the per-shard stats are all-gathered and merged,
+        so every rank computes the same score and takes the same fire decision."""
+        x = logits if rows is None else logits[rows]
+        st = self.row_stats(x)
+        if tp_group is not None:
+            import torch.distributed as dist
+            parts = [torch.empty_like(st) for _ in range(dist.get_world_size(tp_group))]
+            dist.all_gather(parts, st.contiguous(), group=tp_group)
+            st = self.merge_stats(torch.stack(parts))
+        return self.score_stats(st)
 
     def should_fire(self, score: float) -> bool:
         fire = score <= self.tau
