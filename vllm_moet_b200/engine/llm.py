@@ -53,7 +53,12 @@ class LLM:
                  delta_slots: int = 0, gate: Optional[bool] = None, expert_parallel: bool = False,
                  expert_store: str = "pinned", expert_store_dir: Optional[str] = None, sp_group=None,
                  dcp_group=None, dcp_interleave: int = 1, **model_overrides):
-        cfg = get_preset(model, **model_overrides) if isinstance(model, str) else model
+        from ..models.loader import hf_config, is_checkpoint_dir, load_weights
+        ckpt = model if is_checkpoint_dir(model) else None
+        if ckpt is not None:
+            cfg = hf_config(ckpt, **model_overrides)
+        else:
+            cfg = get_preset(model, **model_overrides) if isinstance(model, str) else model
         if (sp_group is not None or dcp_group is not None) and (tp_group is not None or pp_group is not None):
             raise ValueError("context parallelism here runs on replicated weights (no TP / PP group)")
         if sp_group is not None and dcp_group is not None:
@@ -87,8 +92,14 @@ class LLM:
             from ..residency import PlanesCache, checkpoint_id
             from ..residency.sources import PlanesSource
             self.expert_source = PlanesSource(PlanesCache(
-                self.ecfg.moet.planes_cache, self.ecfg.moet.ckpt_id or checkpoint_id(cfg=cfg, seed=seed),
+                self.ecfg.moet.planes_cache,
+                self.ecfg.moet.ckpt_id or (checkpoint_id(model_path=ckpt) if ckpt else checkpoint_id(cfg=cfg, seed=seed)),
                 tp_world=tensor_parallel_size, tp_rank=tp_rank))
+        if weights is None and ckpt is not None:
+            weights = load_weights(ckpt, cfg, self.device, tp_rank=tp_rank, tp_size=tensor_parallel_size,
+                                   with_mtp=num_speculative_tokens > 0, pp_rank=pp_rank,
+                                   pp_size=pipeline_parallel_size, expert_parallel=expert_parallel,
+                                   expert_source=self.expert_source)
         self.mw = weights if weights is not None else random_weights(
             cfg, self.device, seed=seed, tp_rank=tp_rank, tp_size=tensor_parallel_size,
             with_mtp=num_speculative_tokens > 0, pp_rank=pp_rank, pp_size=pipeline_parallel_size,
