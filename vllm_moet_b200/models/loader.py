@@ -173,6 +173,10 @@ def _layer(rd: CheckpointReader, cfg: ModelConfig, li: int, dev, moe: bool, tp_r
     if isinstance(lw.kv_b, Fp8Linear):
         lw.w_uk_t, lw.w_uv = _derive_absorb(lw.kv_b, cfg, Hh)
     if cfg.index_heads:
+        if rd.has(P + "self_attn.indexer.k_norm.weight"):
+            raise NotImplementedError("indexer with a key LayerNorm (DeepSeek-V3.2 layout): this engine's DSA "
+                                      "indexer has no key norm or indexer rope, so the checkpoint would be "
+                                      "served as a different model")
         lw.idx_wq = rd.linear(P + "self_attn.indexer.wq_b", dt)
         lw.idx_wk = rd.linear(P + "self_attn.indexer.wk", dt)
         lw.idx_ww = rd.linear(P + "self_attn.indexer.weights_proj", dt)
