@@ -189,3 +189,21 @@ def test_tp2_slices_of_the_checkpoint_match_one_rank(tmp_path):
     want = LLM(str(tmp_path), device="cpu", num_speculative_tokens=1, max_model_len=128).generate(
         [[5, 9, 17, 33, 65]], SamplingParams(max_tokens=6, ignore_eos=True))[0].outputs[0].token_ids
     assert run_ranks(_tp_ckpt, 2, str(tmp_path)) == [want, want]
+
+
+def test_checkpoint_tokenizer_is_used(tmp_path):
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    _make_ckpt(str(tmp_path), quant=False)
+    words = ["<s>", "</s>", "<pad>"] + [f"w{i}" for i in range(100)]
+    tk = Tokenizer(models.WordLevel({w: i for i, w in enumerate(words)}, unk_token="<pad>"))
+    tk.pre_tokenizer = pre_tokenizers.Whitespace()
+    PreTrainedTokenizerFast(tokenizer_object=tk, bos_token="<s>", eos_token="</s>", pad_token="<pad>") \
+        .save_pretrained(str(tmp_path))
+    llm = LLM(str(tmp_path), device="cpu", num_speculative_tokens=1, max_model_len=128)
+    assert llm.tokenizer.encode("w5 w7") == [8, 10] and llm.tokenizer.eos_token_id == 1
+    out = llm.generate(["w5 w7 w9"], SamplingParams(max_tokens=4, ignore_eos=True))[0]
+    assert out.prompt_token_ids == [0, 8, 10, 12]
+    assert out.outputs[0].text == llm.tokenizer.decode(out.outputs[0].token_ids)

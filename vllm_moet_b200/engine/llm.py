@@ -23,7 +23,7 @@ from ..config import EngineConfig, ModelConfig, MoetConfig, ParallelConfig, get_
 from ..models.weights import ModelWeights, random_weights
 from .kv_manager import BlockManager
 from .sampling_params import CompletionOutput, RequestOutput, SamplingParams, cut_at_stop
-from .tokenizer import ByteTokenizer
+from .tokenizer import ByteTokenizer, tokenizer_for
 
 
 @dataclass
@@ -82,7 +82,7 @@ class LLM:
                                  max_num_seqs=max_num_seqs, max_model_len=max_model_len,
                                  kv_cache_dtype=kv_cache_dtype, num_speculative_tokens=num_speculative_tokens,
                                  cuda_graphs=cuda_graphs, seed=seed, device=str(self.device))
-        self.tokenizer = ByteTokenizer(cfg.vocab)
+        self.tokenizer = tokenizer_for(cfg.vocab, ckpt)
         if self.device.type == "cuda" and weights is None and not expert_cache_slots \
                 and self.ecfg.moet.base_cache_gb <= 0 and not self.ecfg.moet.force_resident:
             self._resident_hardstop(cfg, tensor_parallel_size, expert_parallel, num_layers)
