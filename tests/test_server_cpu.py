@@ -172,3 +172,48 @@ def test_logprobs_over_http(server):
     assert len(content) == 3 and all(len(e["top_logprobs"]) == 2 and e["logprob"] <= 0 for e in content)
     plain = requests.post(url + "/v1/completions", json={"prompt": [5, 6], "max_tokens": 2}, timeout=120).json()
     assert plain["choices"][0]["logprobs"] is None
+
+
+def test_cli_flags_map_to_engine_arguments():
+    from vllm_moet_b200.entrypoints.openai_server import build_parser, llm_kwargs
+    a = build_parser().parse_args(["--model", "tiny-moe", "--speculative-config",
+                                   '{"method": "deepseek_mtp", "num_speculative_tokens": 3}',
+                                   "--kv-cache-dtype", "nvfp4", "--enable-expert-parallel", "--reasoning-parser",
+                                   "none", "--served-model-name", "moet", "--gpu-memory-utilization", "0.9"])
+    kw = llm_kwargs(a)
+    assert kw["num_speculative_tokens"] == 3 and kw["kv_cache_dtype"] == "nvfp4" and kw["expert_parallel"]
+    assert a.reasoning_parser == "none" and a.served_model_name == "moet"
+    for bad in (["--speculative-config", '{"method": "eagle"}'], ["--pipeline-parallel-size", "2"],
+                ["--decode-context-parallel-size", "2"]):
+        with pytest.raises(SystemExit):
+            llm_kwargs(build_parser().parse_args(bad))
+
+
+def test_raw_content_without_parsers():
+    """--reasoning-parser none / --tool-call-parser none: chat content is the raw completion."""
+    import uvicorn
+    from vllm_moet_b200.engine.llm import LLM
+    from vllm_moet_b200.entrypoints.openai_server import EngineWorker, build_app
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+    w = EngineWorker(llm, "raw")
+    port = _free_port()
+    srv = uvicorn.Server(uvicorn.Config(build_app(w, None, None), host="127.0.0.1", port=port, log_level="warning"))
+    th = threading.Thread(target=srv.run, daemon=True)
+    th.start()
+    url = f"http://127.0.0.1:{port}"
+    try:
+        for _ in range(100):
+            try:
+                if requests.get(url + "/health", timeout=1).ok:
+                    break
+            except requests.ConnectionError:
+                time.sleep(0.1)
+        r = requests.post(url + "/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}],
+                                                              "max_tokens": 4, "ignore_eos": True}, timeout=120)
+        msg = r.json()["choices"][0]["message"]
+        assert msg["role"] == "assistant" and "reasoning_content" not in msg and "tool_calls" not in msg
+        assert r.json()["model"] == "raw"
+    finally:
+        srv.should_exit = True
+        th.join(timeout=10)
+        w.close()

@@ -145,7 +145,11 @@ class _StopStream:
         return out
 
 
-def build_app(worker: EngineWorker):
+def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_v4",
+              tool_call_parser: Optional[str] = "deepseek_v4"):
+    """The HTTP app.  Parsers (the reference's --reasoning-parser / --tool-call-parser):
+    "deepseek_v4" splits chat output into reasoning_content / content / tool_calls with the
+    DS4 encoding; None returns the raw completion text as content."""
     from fastapi import FastAPI, HTTPException
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
@@ -298,10 +302,14 @@ def build_app(worker: EngineWorker):
             return StreamingResponse(gen(), media_type="text/event-stream")
         ids, finish, lps = await collect(aq)
         out_text = cut_at_stop(tok.decode(ids), params.stop, params.include_stop_str_in_output)[0]
-        try:
-            msg = chat_encoding.parse_completion(out_text, thinking=thinking)
-        except ValueError:
-            msg = {"role": "assistant", "content": out_text}     # a free-form completion (random-init models)
+        msg = {"role": "assistant", "content": out_text}
+        if reasoning_parser or tool_call_parser:
+            try:
+                msg = chat_encoding.parse_completion(out_text, thinking=thinking and bool(reasoning_parser))
+                if not tool_call_parser and msg.get("tool_calls"):
+                    msg = {"role": "assistant", "content": out_text}
+            except ValueError:
+                pass        # a free-form completion (random-init models): returned as content
         return JSONResponse({"id": rid, "object": "chat.completion", "created": created, "model": name,
                              "choices": [{"index": 0, "message": msg, "finish_reason": finish,
                                           "logprobs": chat_logprobs(ids, lps, params.logprobs)
@@ -312,22 +320,63 @@ def build_app(worker: EngineWorker):
     return app
 
 
-def main(argv=None):
-    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
-    ap.add_argument("--model", default="ds4-flash-shape")
+_PARSERS = ("deepseek_v4", "none")
+
+
+def build_parser():
+    ap = argparse.ArgumentParser(description="OpenAI-compatible server over the engine")
+    ap.add_argument("--model", default="ds4-flash-shape", help="a preset name or a local checkpoint directory")
+    ap.add_argument("--served-model-name", default=None)
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
     ap.add_argument("--num-layers", type=int, default=None)
     ap.add_argument("--max-model-len", type=int, default=8192)
     ap.add_argument("--max-num-seqs", type=int, default=32)
     ap.add_argument("--num-speculative-tokens", type=int, default=2)
+    ap.add_argument("--speculative-config", default=None,
+                    help='JSON, e.g. {"method": "mtp", "num_speculative_tokens": 2}')
+    ap.add_argument("--kv-cache-dtype", default="auto", choices=("auto", "bf16", "bfloat16", "nvfp4"))
     ap.add_argument("--device", default=None)
     ap.add_argument("--data-parallel-size", type=int, default=1,
                     help="replicated engines behind a request router (see dp_serve)")
     ap.add_argument("--tensor-parallel-size", type=int, default=None,
                     help="GPUs per replica with --data-parallel-size; otherwise torchrun's WORLD_SIZE")
+    ap.add_argument("--pipeline-parallel-size", type=int, default=1)
+    ap.add_argument("--decode-context-parallel-size", type=int, default=1)
+    ap.add_argument("--enable-expert-parallel", action="store_true")
     ap.add_argument("--gpus", default=None, help="GPU ids for the replicas of --data-parallel-size ('cpu': none)")
-    args = ap.parse_args(argv)
+    ap.add_argument("--reasoning-parser", default="deepseek_v4", choices=_PARSERS)
+    ap.add_argument("--tool-call-parser", default="deepseek_v4", choices=_PARSERS)
+    ap.add_argument("--enable-auto-tool-choice", action="store_true", help="accepted (tools are always parsed)")
+    ap.add_argument("--gpu-memory-utilization", type=float, default=None, help="accepted; KV blocks are sized "
+                    "from the free memory after the weights")
+    ap.add_argument("--trust-remote-code", action="store_true", help="accepted; no remote code is run")
+    ap.add_argument("--dtype", default="auto", help="accepted; activations are bf16")
+    return ap
+
+
+def llm_kwargs(args, world: int = 1, rank: int = 0, group=None) -> dict:
+    """Server flags -> LLM keyword arguments (refusing what the GPU server path does not serve)."""
+    k = args.num_speculative_tokens
+    if args.speculative_config:
+        spec = json.loads(args.speculative_config)
+        method = spec.get("method", "mtp")
+        if method not in ("mtp", "deepseek_mtp", "deepseek_v4_mtp"):
+            raise SystemExit(f"speculative method {method!r}: this engine drafts with the model's MTP module")
+        k = int(spec.get("num_speculative_tokens", k))
+    if args.pipeline_parallel_size != 1:
+        raise SystemExit("--pipeline-parallel-size: the server runs TP ranks; use the LLM API for pipeline stages")
+    if args.decode_context_parallel_size != 1:
+        raise SystemExit("--decode-context-parallel-size: DCP runs on the CPU engine only so far")
+    kv = "nvfp4" if args.kv_cache_dtype == "nvfp4" else "bf16"
+    return dict(device=args.device, num_speculative_tokens=k, max_model_len=args.max_model_len,
+                max_num_seqs=args.max_num_seqs, num_layers=args.num_layers, kv_cache_dtype=kv,
+                tensor_parallel_size=world, tp_group=group, tp_rank=rank,
+                expert_parallel=bool(args.enable_expert_parallel))
+
+
+def main(argv=None):
+    args = build_parser().parse_args(argv)
     if args.data_parallel_size > 1:
         import sys
         from .dp_serve import main as dp_main
@@ -340,21 +389,24 @@ def main(argv=None):
     if args.tensor_parallel_size not in (None, world):
         raise SystemExit(f"--tensor-parallel-size {args.tensor_parallel_size} without --data-parallel-size: "
                          f"launch with torchrun --nproc-per-node {args.tensor_parallel_size}")
+    kw = llm_kwargs(args, world, rank)
     group = None
     if world > 1:
         import torch.distributed as dist
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         dist.init_process_group("nccl")
         group = dist.group.WORLD
-    llm = LLM(args.model, device=args.device, num_speculative_tokens=args.num_speculative_tokens,
-              max_model_len=args.max_model_len, max_num_seqs=args.max_num_seqs, num_layers=args.num_layers,
-              tensor_parallel_size=world, tp_group=group, tp_rank=rank)
+        kw["tp_group"] = group
+    llm = LLM(args.model, **kw)
     if rank != 0:
         follower_loop(llm, group)
         return
     import uvicorn
-    worker = EngineWorker(llm, args.model, group, max_batch=args.max_num_seqs)
-    uvicorn.run(build_app(worker), host=args.host, port=args.port, log_level="warning")
+    name = args.served_model_name or args.model
+    worker = EngineWorker(llm, name, group, max_batch=args.max_num_seqs)
+    parse = lambda v: None if v == "none" else v      # noqa: E731
+    uvicorn.run(build_app(worker, parse(args.reasoning_parser), parse(args.tool_call_parser)), host=args.host,
+                port=args.port, log_level="warning")
 
 
 if __name__ == "__main__":
