@@ -159,3 +159,29 @@ def test_logprobs_match_reference():
                  callbacks=[lambda ids, fin, lp=None: got.extend(lp or [])])
     assert len(got) == 3 and all(len(d) == 1 for d in got)
     assert llm.generate([p], SamplingParams(max_tokens=2))[0].outputs[0].logprobs is None
+
+
+def test_requests_join_and_abort_between_steps():
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256, max_num_seqs=4)
+    sp = SamplingParams(max_tokens=12, ignore_eos=True)
+    solo = {n: llm.generate([p], s)[0].outputs[0].token_ids for n, p, s in
+            (("b", [8, 9], sp), ("j", [9, 10, 11], SamplingParams(max_tokens=5, ignore_eos=True)))}
+    ev = {}
+
+    def cb(name):
+        return lambda ids, fin, lp=None: ev.setdefault(name, []).append((list(ids), fin))
+    step = [0]
+
+    def between(n_free):
+        step[0] += 1
+        new = [("j", [9, 10, 11], SamplingParams(max_tokens=5, ignore_eos=True), cb("j"))] if step[0] == 3 else []
+        return new, ({"a"} if step[0] == 2 else set())
+    out = llm.generate([[5, 6, 7], [8, 9]], sp, callbacks=[cb("a"), cb("b")], request_ids=["a", "b"],
+                       between_steps=between)
+    a, b = (o.outputs[0] for o in out)
+    assert a.finish_reason == "abort" and len(a.token_ids) < 12 and ev["a"][-1][1] == "abort"
+    assert b.finish_reason == "length" and b.token_ids == solo["b"]
+    joined = sum((ids for ids, _ in ev["j"]), [])
+    assert joined == solo["j"] and ev["j"][-1][1] == "length"

@@ -217,3 +217,33 @@ def test_raw_content_without_parsers():
         srv.should_exit = True
         th.join(timeout=10)
         w.close()
+
+
+def test_requests_join_running_batch_and_disconnect_aborts(server):
+    url, _ = server
+    order = []
+
+    def run(name, n):
+        r = requests.post(url + "/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": n, "ignore_eos": True},
+                          timeout=120)
+        assert r.ok
+        order.append(name)
+    long = threading.Thread(target=run, args=("long", 120))
+    long.start()
+    time.sleep(0.3)
+    run("short", 2)                  # joins the running batch instead of waiting for it
+    long.join()
+    assert order == ["short", "long"]
+    # a streaming client that goes away aborts its request
+    s = requests.post(url + "/v1/completions", json={"prompt": [5, 6], "max_tokens": 200, "ignore_eos": True,
+                                                     "stream": True}, stream=True, timeout=120)
+    it = s.iter_lines()
+    next(it)
+    s.close()
+    m = ""
+    for _ in range(100):
+        m = requests.get(url + "/metrics").text
+        if "moet_aborted_total 1" in m:
+            break
+        time.sleep(0.1)
+    assert "moet_aborted_total 1" in m

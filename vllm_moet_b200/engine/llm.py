@@ -302,31 +302,46 @@ class LLM:
                 raise ValueError("prompt token id out of range")
         return out
 
+    def _check_request(self, t, sp):
+        if sp.logprobs is not None and self.device.type == "cuda" and self._tp_group is not None:
+            raise NotImplementedError("logprobs under tensor parallelism: each rank holds a vocab shard")
+        if sp.temperature != 0 and self.device.type == "cuda":
+            raise NotImplementedError("temperature > 0: the GPU runner verifies drafts greedily inside the "
+                                      "decode graph; sampling is served by the CPU engine")
+        if len(t) + sp.max_tokens + self.k + 1 > self.ecfg.max_model_len:
+            raise ValueError(f"prompt ({len(t)}) + max_tokens ({sp.max_tokens}) exceeds max_model_len")
+
     def generate(self, prompts, sampling_params: Union[SamplingParams, Sequence[SamplingParams], None] = None,
-                 use_tqdm: bool = False, callbacks: Optional[Sequence] = None) -> List[RequestOutput]:
+                 use_tqdm: bool = False, callbacks: Optional[Sequence] = None, request_ids: Optional[Sequence] = None,
+                 between_steps=None) -> List[RequestOutput]:
         """Generation for a batch of prompts (str, token-id lists or
         {"prompt_token_ids": [...]}).  `callbacks[i](new_ids, finish_reason)` is
-        called as tokens of prompt i are emitted (streaming)."""
+        called as tokens of prompt i are emitted (streaming).
+
+        `between_steps(n_free) -> (new, abort_ids)` (serving): called before every
+        step; `new` = [(request_id, prompt_ids, params, callback)] requests that join
+        the running batch (at most n_free: the batch size of the running CUDA-graph
+        bucket), `abort_ids` = request ids to finish now with reason "abort".  Joined
+        requests report through their callbacks only."""
         toks = self._normalize(prompts)
         if sampling_params is None:
             sampling_params = SamplingParams()
         if isinstance(sampling_params, SamplingParams):
             sampling_params = [sampling_params] * len(toks)
         reqs = []
-        for t, sp in zip(toks, sampling_params):
-            if sp.logprobs is not None and self.device.type == "cuda" and self._tp_group is not None:
-                raise NotImplementedError("logprobs under tensor parallelism: each rank holds a vocab shard")
-            if sp.temperature != 0 and self.device.type == "cuda":
-                raise NotImplementedError("temperature > 0: the GPU runner verifies drafts greedily inside the "
-                                          "decode graph; sampling is served by the CPU engine")
-            if len(t) + sp.max_tokens + self.k + 1 > self.ecfg.max_model_len:
-                raise ValueError(f"prompt ({len(t)}) + max_tokens ({sp.max_tokens}) exceeds max_model_len")
-            reqs.append(_Req(f"req-{next(self._ids)}", t, sp, t_arrive=time.perf_counter(),
+        for i, (t, sp) in enumerate(zip(toks, sampling_params)):
+            self._check_request(t, sp)
+            rid = request_ids[i] if request_ids is not None else f"req-{next(self._ids)}"
+            reqs.append(_Req(rid, t, sp, t_arrive=time.perf_counter(),
                              callback=callbacks[len(reqs)] if callbacks is not None else None))
-        if self.device.type == "cuda":
-            self._run_native(reqs)
-        else:
-            self._run_torch(reqs)
+        self._between = between_steps
+        try:
+            if self.device.type == "cuda":
+                self._run_native(reqs)
+            else:
+                self._run_torch(reqs)
+        finally:
+            self._between = None
         return [RequestOutput(r.rid, r.prompt, [CompletionOutput(
                     0, r.text if r.text is not None else self.tokenizer.decode(r.out), r.out, r.finish, r.stop_reason,
                     r.logprobs, (sum(d[t] for d, t in zip(r.logprobs, r.out)) if r.logprobs is not None else None))],
@@ -373,12 +388,47 @@ class LLM:
                 r.callback(r.out[n0:], r.finish)
         return r.finish is not None
 
+    def _poll(self, waiting, rows, n_free, release):
+        """Serving hook: admit joined requests into `waiting`, finish aborted ones."""
+        hook = getattr(self, "_between", None)
+        if hook is None:
+            return
+        new, aborts = hook(n_free)
+        for rid, prompt, sp, cb in new:
+            try:
+                self._check_request(prompt, sp)
+            except (ValueError, NotImplementedError) as e:
+                if cb is not None:
+                    cb([], "error:" + str(e))
+                continue
+            waiting.append(_Req(rid, list(prompt), sp, t_arrive=time.perf_counter(), callback=cb))
+        if not aborts:
+            return
+        for r in [r for r in waiting if r.rid in aborts]:
+            waiting.remove(r)
+            r.finish = "abort"
+            if r.callback is not None:
+                r.callback([], "abort")
+        for r in list(rows):
+            if r is not None and r.rid in aborts and not r.finish:
+                r.finish, r.t_done = "abort", time.perf_counter()
+                if r.callback is not None:
+                    r.callback([], "abort")
+                release(r)
+
     def _run_torch(self, reqs):
         waiting = deque(reqs)
-        B = max(1, min(len(reqs), self.ecfg.max_num_seqs))
+        # serving: room for requests that join between steps (rows cost nothing on the CPU engine)
+        B = self.ecfg.max_num_seqs if self._between is not None else max(1, min(len(reqs), self.ecfg.max_num_seqs))
         rows = [None] * B
         steps = accepted = 0
-        while waiting or any(rows):
+        def release(r):
+            rows[r.row] = None
+            self.runner.release(r.row)
+        while True:
+            self._poll(waiting, rows, sum(r is None for r in rows) - len(waiting), release)
+            if not (waiting or any(rows)):
+                break
             free = [i for i, r in enumerate(rows) if r is None]
             adm = []
             while waiting and free:
@@ -423,7 +473,11 @@ class LLM:
         t_decode = 0.0
         graph = runner.graphs.get(B) if self.ecfg.cuda_graphs else None
         bt_host = torch.zeros(B, self.max_blocks, dtype=torch.int32)
-        while waiting or any(r is not None for r in rows):
+        while True:
+            self._poll(waiting, rows, sum(r is None for r in rows) - len(waiting),
+                       lambda r: self._finish_row(r, rows))
+            if not (waiting or any(r is not None for r in rows)):
+                break
             free = [i for i, r in enumerate(rows) if r is None]
             adm = []
             while waiting and free and self.blocks.can_allocate(len(waiting[0].prompt) + waiting[0].params.max_tokens + kp1 + 1):

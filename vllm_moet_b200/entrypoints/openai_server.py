@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import argparse
 import asyncio
+import itertools
 import json
 import os
 import queue
@@ -32,19 +33,32 @@ from . import chat_encoding
 
 
 class EngineWorker:
-    """Owns the LLM on one thread; requests come in through a queue."""
+    """Owns the LLM on one thread; requests come in through a queue.  A request that
+    arrives while a batch is decoding joins it between steps (up to the running batch
+    size); `abort(request_id)` finishes a request at the next step."""
 
     def __init__(self, llm, model_name: str, tp_group=None, max_batch: int = 32):
         self.llm, self.model_name, self.group = llm, model_name, tp_group
         self.max_batch = max_batch
         self.q: "queue.Queue" = queue.Queue()
-        self.stats = {"requests": 0, "prompt_tokens": 0, "generated_tokens": 0, "batches": 0}
+        self.stats = {"requests": 0, "prompt_tokens": 0, "generated_tokens": 0, "batches": 0, "joined": 0,
+                      "aborted": 0}
+        self._ids = itertools.count()
+        self._aborts: set = set()
+        self._lock = threading.Lock()
         self._stop = False
         self.thread = threading.Thread(target=self._loop, name="engine", daemon=True)
         self.thread.start()
 
-    def submit(self, prompt_ids: List[int], params: SamplingParams, on_tokens) -> None:
-        self.q.put((prompt_ids, params, on_tokens))
+    def submit(self, prompt_ids: List[int], params: SamplingParams, on_tokens) -> str:
+        rid = f"srv-{next(self._ids)}"
+        self.q.put((rid, prompt_ids, params, on_tokens))
+        return rid
+
+    def abort(self, rid: str) -> None:
+        with self._lock:
+            self._aborts.add(rid)
+        self.stats["aborted"] += 1
 
     def _loop(self):
         while not self._stop:
@@ -66,21 +80,45 @@ class EngineWorker:
             import torch.distributed as dist
             dist.broadcast_object_list([None], src=0, group=self.group)
 
-    def _run(self, batch):
-        prompts = [b[0] for b in batch]
-        params = [b[1] for b in batch]
+    def _between(self, n_free: int):
+        """Serving hook of LLM.generate: requests that arrived meanwhile, aborts."""
+        items = []
+        while len(items) < n_free and not self._stop:
+            try:
+                it = self.q.get_nowait()
+            except queue.Empty:
+                break
+            if it is None:              # shutdown: finish the running batch first
+                self._stop = True
+                break
+            items.append(it)
+        with self._lock:
+            aborts, self._aborts = self._aborts, set()
+        self.stats["joined"] += len(items)
+        self.stats["requests"] += len(items)
+        self.stats["prompt_tokens"] += sum(len(it[1]) for it in items)
         if self.group is not None:
             import torch.distributed as dist
-            dist.broadcast_object_list([(prompts, params)], src=0, group=self.group)
+            dist.broadcast_object_list([([it[:3] for it in items], aborts)], src=0, group=self.group)
+        return items, aborts
+
+    def _run(self, batch):
+        rids = [b[0] for b in batch]
+        prompts = [b[1] for b in batch]
+        params = [b[2] for b in batch]
+        if self.group is not None:
+            import torch.distributed as dist
+            dist.broadcast_object_list([(prompts, params, rids)], src=0, group=self.group)
         self.stats["batches"] += 1
         self.stats["requests"] += len(batch)
         self.stats["prompt_tokens"] += sum(len(p) for p in prompts)
         try:
-            outs = self.llm.generate(prompts, params, callbacks=[b[2] for b in batch])
+            outs = self.llm.generate(prompts, params, callbacks=[b[3] for b in batch], request_ids=rids,
+                                     between_steps=self._between)
             self.stats["generated_tokens"] += sum(len(o.outputs[0].token_ids) for o in outs)
         except Exception as e:  # noqa: BLE001 - report to every waiting request
             for b in batch:
-                b[2]([], "error:" + str(e))
+                b[3]([], "error:" + str(e))
 
     def close(self):
         self.q.put(None)
@@ -88,15 +126,22 @@ class EngineWorker:
 
 
 def follower_loop(llm, tp_group):
-    """Ranks > 0 under TP: run each broadcast batch in lock step with rank 0."""
+    """Ranks > 0 under TP: run each broadcast batch in lock step with rank 0, including
+    the requests that join it and the aborts (received at the same points of the loop)."""
     import torch.distributed as dist
+
+    def between(n_free):
+        box = [None]
+        dist.broadcast_object_list(box, src=0, group=tp_group)
+        items, aborts = box[0]
+        return [(rid, p, sp, None) for rid, p, sp in items], aborts
     while True:
         box = [None]
         dist.broadcast_object_list(box, src=0, group=tp_group)
         if box[0] is None:
             return
-        prompts, params = box[0]
-        llm.generate(prompts, params)
+        prompts, params, rids = box[0]
+        llm.generate(prompts, params, request_ids=rids, between_steps=between)
 
 
 def _params_from(body: Dict[str, Any], default_max: int = 16) -> SamplingParams:
@@ -164,8 +209,19 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
 
         def cb(ids, finish, lp=None):
             loop.call_soon_threadsafe(aq.put_nowait, (list(ids), finish, lp))
-        worker.submit(prompt_ids, params, cb)
+        aq.rid = worker.submit(prompt_ids, params, cb)
         return aq
+
+    async def guard(agen, aq):
+        """Stream `agen`; a client that goes away before the end aborts its request."""
+        done = False
+        try:
+            async for chunk in agen:
+                yield chunk
+            done = True
+        finally:
+            if not done:
+                worker.abort(aq.rid)
 
     async def collect(aq):
         ids, finish, lps = [], None, []
@@ -256,7 +312,7 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
                                           "finish_reason": finish}]}
                     yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
-            return StreamingResponse(gen(), media_type="text/event-stream")
+            return StreamingResponse(guard(gen(), aq), media_type="text/event-stream")
         qs = [run_request(p, params) for p in plist]
         choices, n_out = [], 0
         for i, aq in enumerate(qs):
@@ -299,7 +355,7 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
                              "choices": [{"index": 0, "delta": delta, "finish_reason": finish}]}
                     yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
-            return StreamingResponse(gen(), media_type="text/event-stream")
+            return StreamingResponse(guard(gen(), aq), media_type="text/event-stream")
         ids, finish, lps = await collect(aq)
         out_text = cut_at_stop(tok.decode(ids), params.stop, params.include_stop_str_in_output)[0]
         msg = {"role": "assistant", "content": out_text}
