@@ -86,7 +86,11 @@ def test_completions_match_engine(server):
     assert body["choices"][0]["token_ids"] == reference.greedy_generate(llm.mw, [5, 6, 7, 8], 6)
     assert body["usage"]["completion_tokens"] == 6
     assert requests.get(url + "/v1/models").json()["data"][0]["id"] == "tiny-moe"
-    assert "moet_requests_total" in requests.get(url + "/metrics").text
+    m = requests.get(url + "/metrics").text
+    assert "moet_requests_total" in m
+    assert "moet_time_to_first_token_seconds_count" in m and "moet_e2e_request_latency_seconds_bucket" in m
+    count = [ln for ln in m.splitlines() if ln.startswith("moet_e2e_request_latency_seconds_count")][0]
+    assert float(count.split()[-1]) >= 1
 
 
 def test_streaming_and_chat(server):

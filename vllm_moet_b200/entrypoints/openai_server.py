@@ -202,12 +202,32 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
     tok = worker.llm.tokenizer
     name = worker.model_name
 
+    from prometheus_client import CollectorRegistry, Histogram, generate_latest
+    registry = CollectorRegistry()
+    buckets = (0.005, 0.01, 0.02, 0.05, 0.1, 0.2, 0.5, 1, 2, 5, 10, 30, 60)
+    h_ttft = Histogram("moet_time_to_first_token_seconds", "time to first token", registry=registry,
+                       buckets=buckets)
+    h_tpot = Histogram("moet_time_per_output_token_seconds", "time per output token after the first",
+                       registry=registry, buckets=(0.001, 0.002, 0.005, 0.01, 0.02, 0.05, 0.1, 0.2, 0.5, 1))
+    h_e2e = Histogram("moet_e2e_request_latency_seconds", "end-to-end request latency", registry=registry,
+                      buckets=buckets)
+
     def run_request(prompt_ids, params):
-        """-> (asyncio.Queue of (ids, finish)) fed from the engine thread."""
+        """-> (asyncio.Queue of (ids, finish, logprobs)) fed from the engine thread."""
         loop = asyncio.get_running_loop()
         aq: "asyncio.Queue" = asyncio.Queue()
+        t0, seen = time.perf_counter(), {"first": None, "n": 0}
 
         def cb(ids, finish, lp=None):
+            now = time.perf_counter()
+            if ids and seen["first"] is None:
+                seen["first"] = now
+                h_ttft.observe(now - t0)
+            seen["n"] += len(ids)
+            if finish is not None and not finish.startswith("error:"):
+                h_e2e.observe(now - t0)
+                if seen["first"] is not None and seen["n"] > 1:
+                    h_tpot.observe((now - seen["first"]) / (seen["n"] - 1))
             loop.call_soon_threadsafe(aq.put_nowait, (list(ids), finish, lp))
         aq.rid = worker.submit(prompt_ids, params, cb)
         return aq
@@ -266,7 +286,7 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
     @app.get("/metrics")
     async def metrics():
         lines = [f"moet_{k}_total {v}" for k, v in worker.stats.items()]
-        return PlainTextResponse("\n".join(lines) + "\n")
+        return PlainTextResponse("\n".join(lines) + "\n" + generate_latest(registry).decode())
 
     def _servable(params):
         if params.temperature > 0 and worker.llm.device.type == "cuda":
