@@ -141,8 +141,18 @@ def main():
     st_e2e = dict(llm.stats)
     e2e_tok_s = (len(outs[0].outputs[0].token_ids) - 1) / maxr(st_e2e["decode_s"])
 
-    extra = {}
-    if not args.skip_extra:
+    extra, errors = {}, {}
+
+    def secondary(name, fn):
+        """A secondary measurement that fails (the same way on every rank) is reported as an
+        error field; the headline number above stands."""
+        try:
+            fn()
+        except Exception as e:  # noqa: BLE001
+            errors[name] = f"{type(e).__name__}: {str(e)[:200]}"
+            torch.cuda.synchronize()
+
+    def streams():
         # ---- 32-stream aggregate decode (public API, device replays inside) ------------------
         S = args.streams
         llm.generate([prompt(args.prompt_len) for _ in range(S)], SamplingParams(max_tokens=4, ignore_eos=True))
@@ -153,26 +163,34 @@ def main():
         dec_s = maxr(stt["decode_s"])
         extra[f"decode_{S}_streams_tok_s"] = gen / dec_s
         extra[f"decode_{S}_streams_steps_s"] = stt["steps"] / dec_s
+
+    def prefill():
         # ---- 8k prefill ----------------------------------------------------------------------
         p8 = prompt(args.prefill_len)
         st1 = llm._state(1)
         blocks = llm.blocks.allocate("pf", args.prefill_len + 16)
-        bt = torch.zeros(1, llm.max_blocks, dtype=torch.int32)
-        bt[0, :len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
-        runner.prefill([p8], [bt[0].tolist()], [0], st1)   # warm-up
-        torch.cuda.synchronize()
-        times = []
-        for _ in range(3):
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            runner.prefill([p8], [bt[0].tolist()], [0], st1)
-            e.record()
+        try:
+            bt = torch.zeros(1, llm.max_blocks, dtype=torch.int32)
+            bt[0, :len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
+            runner.prefill([p8], [bt[0].tolist()], [0], st1)   # warm-up
             torch.cuda.synchronize()
-            times.append(s.elapsed_time(e))
-        llm.blocks.release("pf")
+            times = []
+            for _ in range(3):
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                runner.prefill([p8], [bt[0].tolist()], [0], st1)
+                e.record()
+                torch.cuda.synchronize()
+                times.append(s.elapsed_time(e))
+        finally:
+            llm.blocks.release("pf")
         pf_ms = maxr(min(times))
         extra["prefill_8k_tok_s"] = args.prefill_len * 1000.0 / pf_ms
         extra["prefill_8k_ms"] = pf_ms
+
+    if not args.skip_extra:
+        secondary(f"decode_{args.streams}_streams", streams)
+        secondary("prefill_8k", prefill)
 
     if rank == 0:
         out = {
@@ -196,6 +214,8 @@ def main():
             "load_s": round(load_s, 1),
             **{k: round(v, 2) for k, v in extra.items()},
         }
+        if errors:
+            out["errors"] = errors
         print(json.dumps(out), flush=True)
     if world > 1:
         # NCCL teardown with communicators still referenced by captured CUDA graphs
