@@ -52,7 +52,7 @@ class LLM:
                  pipeline_parallel_size: int = 1, pp_group=None, pp_rank: int = 0, expert_cache_slots: int = 0,
                  delta_slots: int = 0, gate: Optional[bool] = None, expert_parallel: bool = False,
                  expert_store: str = "pinned", expert_store_dir: Optional[str] = None, sp_group=None,
-                 dcp_group=None, dcp_interleave: int = 1, **model_overrides):
+                 dcp_group=None, dcp_interleave: int = 1, ep_group=None, **model_overrides):
         from ..models.loader import hf_config, is_checkpoint_dir, load_weights
         ckpt = model if is_checkpoint_dir(model) else None
         if ckpt is not None:
@@ -61,8 +61,10 @@ class LLM:
             cfg = get_preset(model, **model_overrides) if isinstance(model, str) else model
         if (sp_group is not None or dcp_group is not None) and (tp_group is not None or pp_group is not None):
             raise ValueError("context parallelism here runs on replicated weights (no TP / PP group)")
-        if sp_group is not None and dcp_group is not None:
-            raise ValueError("choose one of sp_group (SP prefill) and dcp_group (DCP decode)")
+        if sum(g is not None for g in (sp_group, dcp_group, ep_group)) > 1:
+            raise ValueError("choose one of sp_group (SP prefill), dcp_group (DCP decode), ep_group (DP + EP)")
+        if ep_group is not None and (tp_group is not None or pp_group is not None):
+            raise ValueError("ep_group: data-parallel attention with expert-parallel MoE (no TP / PP group)")
         self._mtp_requested = num_speculative_tokens > 0
         if num_layers is not None:
             cfg = cfg.replace(num_layers=num_layers)
@@ -70,8 +72,10 @@ class LLM:
             device = "cuda" if torch.cuda.is_available() else "cpu"
         self.device = torch.device(device)
         self._tp_group, self._pp_group = tp_group, pp_group
-        if self.device.type == "cuda" and (sp_group is not None or dcp_group is not None):
-            raise NotImplementedError("SP prefill / DCP decode run on the CPU engine; the GPU runner has neither yet")
+        if self.device.type == "cuda" and (sp_group is not None or dcp_group is not None or ep_group is not None):
+            raise NotImplementedError("SP prefill / DCP decode / DP+EP run on the CPU engine; the GPU runner has "
+                                      "none of them yet")
+        self._ep_group = ep_group
         if self.device.type == "cuda" and cfg.expert_scale != "ue8m0":
             cfg = cfg.replace(expert_scale="ue8m0")
         if self.device.type == "cuda" and cfg.dense_dtype != "fp8":
@@ -145,8 +149,13 @@ class LLM:
         else:
             from .torch_runner import TorchRunner
             self.blocks = None
+            if ep_group is not None:
+                import torch.distributed as dist
+                from ..parallel.ep import ep_partition
+                ep_partition(self.mw, dist.get_rank(ep_group), dist.get_world_size(ep_group))
             self.runner = TorchRunner(self.mw, self.k, max_model_len, self.device, tp_group=tp_group,
-                                      sp_group=sp_group, dcp_group=dcp_group, dcp_interleave=dcp_interleave)
+                                      sp_group=sp_group, dcp_group=dcp_group, dcp_interleave=dcp_interleave,
+                                      ep_group=ep_group)
 
     def _attach_tracing(self):
         """Prefill span timers, routing capture, delta trace / dump and the gate JSONL
@@ -425,24 +434,43 @@ class LLM:
         def release(r):
             rows[r.row] = None
             self.runner.release(r.row)
+        ep = self._ep_group
+
+        def group_max(v: int) -> int:
+            """DP + EP: every rank makes the same MoE all-to-all calls, so row counts and
+            the loop's end are agreed (MAX) and short ranks run empty rows."""
+            if ep is None:
+                return v
+            import torch.distributed as dist
+            t = torch.tensor([v], dtype=torch.int64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=ep)
+            return int(t)
         while True:
             self._poll(waiting, rows, sum(r is None for r in rows) - len(waiting), release)
-            if not (waiting or any(rows)):
+            if not group_max(int(bool(waiting or any(rows)))):
                 break
             free = [i for i, r in enumerate(rows) if r is None]
             adm = []
             while waiting and free:
                 r = waiting.popleft(); r.row = free.pop(0); rows[r.row] = r; adm.append(r)
+            n_pref = group_max(len(adm))
             if adm:
                 firsts = self.runner.prefill([r.prompt for r in adm], [r.row for r in adm], [r.params for r in adm])
                 for r, f in zip(adm, firsts):
                     r.t_first = time.perf_counter()
                     if self._emit(r, [f], self.runner.last_logits.get(r.row)):
                         rows[r.row] = None; self.runner.release(r.row)
+            if ep is not None:
+                self.runner.dummy_rows(n_pref - len(adm))
             live = [i for i, r in enumerate(rows) if r is not None]
+            n_step = group_max(len(live))
             if not live:
+                if ep is not None:
+                    self.runner.dummy_rows(n_step)
                 continue
             res = self.runner.step(live)
+            if ep is not None:
+                self.runner.dummy_rows(n_step - len(live))
             steps += 1
             for i, (toks, a) in res.items():
                 accepted += a

@@ -12,7 +12,7 @@ from ..models.weights import ModelWeights
 
 class TorchRunner:
     def __init__(self, mw: ModelWeights, k: int, max_len: int, device="cpu", tp_group=None, sp_group=None,
-                 dcp_group=None, dcp_interleave: int = 1):
+                 dcp_group=None, dcp_interleave: int = 1, ep_group=None):
         self.mw = mw
         self.k = k if mw.mtp is not None else 0
         self.dev = torch.device(device)
@@ -23,12 +23,17 @@ class TorchRunner:
         self.sp_group = sp_group        # sequence-parallel prefill ranks: prompt chunks, gathered MLA latents
         self.dcp_group = dcp_group      # decode-context-parallel ranks: KV interleaved by position, LSE merge
         self.dcp_interleave = dcp_interleave
+        self.ep_group = ep_group        # expert parallelism over data-parallel ranks (all-to-all MoE)
 
     def _row(self, r):
         return self.rows[r]
 
     def _ctx(self):
         import contextlib
+        if self.ep_group is not None:
+            from ..parallel.ep import ep_moe_block
+            g = self.ep_group
+            return ref.moe_context(lambda cfg, lw, h: ep_moe_block(cfg, lw, h, g))
         if self.dcp_group is not None:
             from ..parallel.context import dcp_attention_fn
             return ref.attention_context(dcp_attention_fn(self.dcp_group))
@@ -138,6 +143,13 @@ class TorchRunner:
             st["pos"] = p + a + 1
             out[r] = (emitted, a)
         return out
+
+    @torch.no_grad()
+    def dummy_rows(self, n: int):
+        """EP: the MoE collectives of n rows with no tokens (see parallel.ep.ep_dummy_row)."""
+        from ..parallel.ep import ep_dummy_row
+        for _ in range(max(0, n)):
+            ep_dummy_row(self.mw, self.k, self.ep_group)
 
     def release(self, r):
         self.rows.pop(r, None)

@@ -68,6 +68,26 @@ class attention_context:
         _ATTN_IMPL = self.prev
 
 
+_MOE_IMPL = None
+
+
+class moe_context:
+    """Run every MoE block through `fn(cfg, lw, h)` (e.g. expert parallelism with
+    all-to-all dispatch / combine over data-parallel tokens)."""
+
+    def __init__(self, fn):
+        self.fn = fn
+
+    def __enter__(self):
+        global _MOE_IMPL
+        self.prev, _MOE_IMPL = _MOE_IMPL, self.fn
+        return self
+
+    def __exit__(self, *a):
+        global _MOE_IMPL
+        _MOE_IMPL = self.prev
+
+
 def _allreduce(x: torch.Tensor) -> torch.Tensor:
     if _TP_GROUP is not None:
         import torch.distributed as dist
@@ -230,7 +250,7 @@ def decoder_layer(cfg, lw, x, positions, cs, cache=None, li=0):
     h = rms_norm(x, lw.attn_norm, cfg.rms_eps)
     x = x + _allreduce((_ATTN_IMPL or attention)(cfg, lw, h, positions, cs, cache, li))
     h = rms_norm(x, lw.ffn_norm, cfg.rms_eps)
-    return x + _allreduce(moe_block(cfg, lw, h) if lw.is_moe else dense_ffn(cfg, lw, h))
+    return x + _allreduce((_MOE_IMPL or moe_block)(cfg, lw, h) if lw.is_moe else dense_ffn(cfg, lw, h))
 
 
 def forward(mw: ModelWeights, tokens: torch.Tensor, positions: torch.Tensor, cs: torch.Tensor,

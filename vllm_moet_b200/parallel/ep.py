@@ -59,7 +59,7 @@ def ep_combine(y: torch.Tensor, weights: torch.Tensor, state, group) -> torch.Te
     back = _a2a(y, recv_counts, send_counts, group)                 # this rank's rows, in `order`
     pairs = torch.empty_like(back)
     pairs[order] = back                                             # (token, slot) order
-    pairs = pairs.view(T, k, -1) * weights.view(T, k, 1).float()
+    pairs = pairs.view(T, k, back.shape[-1]) * weights.view(T, k, 1).float()     # explicit H: T may be 0
     out = pairs[:, 0]
     for j in range(1, k):                                           # fixed slot order
         out = out + pairs[:, j]
@@ -99,3 +99,42 @@ def dispatch_bytes(T: int, k: int, hidden: int, world: int, elem_bytes: int = 2)
     """Bytes one rank sends per MoE block at uniform routing: (dispatch, combine) off-rank."""
     off = T * k * (world - 1) // world
     return off * hidden * elem_bytes, off * hidden * elem_bytes
+
+
+def ep_partition(mw, rank: int, world: int):
+    """Keep only this rank's expert range [rank * E / W, (rank + 1) * E / W) in every MoE
+    layer (MTP included); attention, dense and shared-expert weights stay replicated."""
+    from ..models.weights import ExpertPool
+    E = mw.cfg.num_experts
+    if E % world:
+        raise ValueError(f"{E} experts do not split evenly over {world} ranks")
+    n = E // world
+    lo = rank * n
+    layers = list(mw.layers) + ([mw.mtp.layer] if mw.mtp is not None else [])
+    for lw in layers:
+        ex = lw.experts
+        if ex is None:
+            continue
+        if ex.dense_w13 is not None:
+            pool, table = ex.pool[:n], torch.arange(n, dtype=torch.int32)
+            d13, d2 = ex.dense_w13[lo:lo + n], ex.dense_w2[lo:lo + n]
+        else:
+            idx = ex.slot_table[lo:lo + n].long()
+            pool, table = ex.pool[idx].contiguous(), torch.arange(n, dtype=torch.int32, device=ex.pool.device)
+            d13 = d2 = None
+        lw.experts = ExpertPool(ex.layout, pool, table, dense_w13=d13, dense_w2=d2, e_lo=lo, n_local=n)
+    return mw
+
+
+def ep_dummy_row(mw, k: int, group) -> None:
+    """The MoE collectives of one engine row with no tokens: a rank with fewer rows than its
+    peers runs these so every rank makes the same sequence of all-to-all calls (each main
+    MoE layer once, then the MTP layer k times)."""
+    cfg = mw.cfg
+    empty = torch.zeros(0, cfg.hidden)
+    for lw in mw.layers:
+        if lw.is_moe:
+            ep_moe_block(cfg, lw, empty, group)
+    if k and mw.mtp is not None:
+        for _ in range(k):
+            ep_moe_block(cfg, mw.mtp.layer, empty, group)
