@@ -185,3 +185,22 @@ def test_requests_join_and_abort_between_steps():
     assert b.finish_reason == "length" and b.token_ids == solo["b"]
     joined = sum((ids for ids, _ in ev["j"]), [])
     assert joined == solo["j"] and ev["j"][-1][1] == "length"
+
+
+def test_n_completions_and_chat():
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+    out = llm.generate([[5, 6, 7], [9, 10]], SamplingParams(max_tokens=5, ignore_eos=True, temperature=1.2, seed=4,
+                                                             n=3))
+    assert len(out) == 2 and all(len(o.outputs) == 3 for o in out)
+    assert [c.index for c in out[0].outputs] == [0, 1, 2]
+    seqs = [c.token_ids for c in out[0].outputs]
+    assert len({tuple(x) for x in seqs}) > 1                      # different seeds, different samples
+    again = llm.generate([[5, 6, 7]], SamplingParams(max_tokens=5, ignore_eos=True, temperature=1.2, seed=4, n=3))
+    assert [c.token_ids for c in again[0].outputs] == seqs         # seed + i per copy: reproducible
+    greedy = llm.generate([[5, 6, 7]], SamplingParams(max_tokens=4, ignore_eos=True, n=2))[0].outputs
+    assert greedy[0].token_ids == greedy[1].token_ids
+    c = llm.chat([{"role": "user", "content": "hi"}], SamplingParams(max_tokens=3, ignore_eos=True))
+    assert len(c) == 1 and len(c[0].outputs[0].token_ids) == 3
+    assert c[0].prompt_token_ids[0] == llm.tokenizer.bos_token_id

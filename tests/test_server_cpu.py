@@ -251,3 +251,15 @@ def test_requests_join_running_batch_and_disconnect_aborts(server):
             break
         time.sleep(0.1)
     assert "moet_aborted_total 1" in m
+
+
+def test_n_choices_over_http(server):
+    url, _ = server
+    body = {"prompt": [5, 6, 7], "max_tokens": 4, "ignore_eos": True, "temperature": 1.3, "seed": 2, "n": 3}
+    ch = requests.post(url + "/v1/completions", json=body, timeout=120).json()["choices"]
+    assert [c["index"] for c in ch] == [0, 1, 2] and len({tuple(c["token_ids"]) for c in ch}) > 1
+    chat = requests.post(url + "/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}],
+                                                             "max_tokens": 3, "ignore_eos": True, "n": 2},
+                         timeout=120).json()
+    assert len(chat["choices"]) == 2 and chat["usage"]["completion_tokens"] == 6
+    assert requests.post(url + "/v1/completions", json=dict(body, stream=True), timeout=120).status_code == 400

@@ -311,6 +311,44 @@ class LLM:
                 raise ValueError("prompt token id out of range")
         return out
 
+    def _generate_n(self, toks, params, callbacks):
+        """n completions per prompt: each prompt is expanded into n requests (copy i samples
+        with seed + i when the request is seeded) and regrouped into one RequestOutput."""
+        import dataclasses
+        flat_t, flat_p, owner = [], [], []
+        for i, (t, sp) in enumerate(zip(toks, params)):
+            for j in range(sp.n):
+                seed = None if sp.seed is None else sp.seed + j
+                flat_t.append(t)
+                flat_p.append(dataclasses.replace(sp, n=1, seed=seed))
+                owner.append(i)
+        cbs = None
+        if callbacks is not None:
+            cbs = [callbacks[i] for i in owner]
+        outs = self.generate(flat_t, flat_p, callbacks=cbs)
+        grouped = []
+        for i, t in enumerate(toks):
+            mine = [o for o, w in zip(outs, owner) if w == i]
+            comps = [dataclasses.replace(o.outputs[0], index=j) for j, o in enumerate(mine)]
+            grouped.append(RequestOutput(mine[0].request_id, t, comps, metrics=mine[0].metrics))
+        return grouped
+
+    def chat(self, messages, sampling_params: Optional[SamplingParams] = None, reasoning_effort: str = "none",
+             tools=None) -> List[RequestOutput]:
+        """One conversation (list of {"role", "content"} messages) or a list of them, rendered
+        with the DeepSeek-V4 chat encoding (a checkpoint tokenizer's own chat template
+        when it has one)."""
+        from ..entrypoints import chat_encoding
+        convs = [messages] if messages and isinstance(messages[0], dict) else list(messages)
+        prompts = []
+        for m in convs:
+            if hasattr(self.tokenizer, "tok") and getattr(self.tokenizer.tok, "chat_template", None):
+                prompts.append(self.tokenizer.apply_chat_template(m))
+            else:
+                text = chat_encoding.render(m, tools=tools, reasoning_effort=reasoning_effort)
+                prompts.append([self.tokenizer.bos_token_id] + self.tokenizer.encode(text))
+        return self.generate(prompts, sampling_params)
+
     def _check_request(self, t, sp):
         if sp.logprobs is not None and self.device.type == "cuda" and self._tp_group is not None:
             raise NotImplementedError("logprobs under tensor parallelism: each rank holds a vocab shard")
@@ -337,6 +375,8 @@ class LLM:
             sampling_params = SamplingParams()
         if isinstance(sampling_params, SamplingParams):
             sampling_params = [sampling_params] * len(toks)
+        if any(sp.n > 1 for sp in sampling_params):
+            return self._generate_n(toks, sampling_params, callbacks)
         reqs = []
         for i, (t, sp) in enumerate(zip(toks, sampling_params)):
             self._check_request(t, sp)

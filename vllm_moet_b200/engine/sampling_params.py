@@ -18,6 +18,7 @@ class SamplingParams:
     include_stop_str_in_output: bool = False
     min_tokens: int = 0             # no stop condition before this many tokens
     logprobs: Optional[int] = None  # per generated token: the chosen token's and the top-N log-probabilities
+    n: int = 1                      # completions per prompt (copies i > 0 sample with seed + i when seeded)
 
     def __post_init__(self):
         if isinstance(self.stop, str):
@@ -27,6 +28,8 @@ class SamplingParams:
             raise ValueError("max_tokens must be >= 1")
         if not 0 <= self.min_tokens <= self.max_tokens:
             raise ValueError("min_tokens must be in [0, max_tokens]")
+        if self.n < 1:
+            raise ValueError("n must be >= 1")
         if self.temperature < 0:
             raise ValueError("temperature must be >= 0")
         if not 0 < self.top_p <= 1:

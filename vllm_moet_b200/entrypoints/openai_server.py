@@ -162,7 +162,7 @@ def _params_from(body: Dict[str, Any], default_max: int = 16) -> SamplingParams:
                           stop_token_ids=stop_ids, ignore_eos=bool(body.get("ignore_eos", False)),
                           stop=[stop] if isinstance(stop, str) else list(stop),
                           include_stop_str_in_output=bool(body.get("include_stop_str_in_output", False)),
-                          min_tokens=int(body.get("min_tokens") or 0), logprobs=lp)
+                          min_tokens=int(body.get("min_tokens") or 0), logprobs=lp, n=int(body.get("n") or 1))
 
 
 class _StopStream:
@@ -288,6 +288,12 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
         lines = [f"moet_{k}_total {v}" for k, v in worker.stats.items()]
         return PlainTextResponse("\n".join(lines) + "\n" + generate_latest(registry).decode())
 
+    def copies(params):
+        """n completions -> n engine requests (copy j samples with seed + j when seeded)."""
+        import dataclasses
+        return [dataclasses.replace(params, n=1, seed=None if params.seed is None else params.seed + j)
+                for j in range(params.n)]
+
     def _servable(params):
         if params.temperature > 0 and worker.llm.device.type == "cuda":
             raise HTTPException(400, "temperature > 0 is served by the CPU engine; the GPU runner decodes greedily")
@@ -313,8 +319,8 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
             plist = [_prompt_ids(prompts)]
         rid, created = f"cmpl-{uuid.uuid4().hex[:24]}", int(time.time())
         if body.get("stream"):
-            if len(plist) != 1:
-                raise HTTPException(400, "streaming serves one prompt per request")
+            if len(plist) != 1 or params.n != 1:
+                raise HTTPException(400, "streaming serves one prompt and one completion per request")
             aq = run_request(plist[0], params)
 
             async def gen():
@@ -333,7 +339,7 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
                     yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(guard(gen(), aq), media_type="text/event-stream")
-        qs = [run_request(p, params) for p in plist]
+        qs = [run_request(p, c) for p in plist for c in copies(params)]
         choices, n_out = [], 0
         for i, aq in enumerate(qs):
             ids, finish, lps = await collect(aq)
@@ -359,7 +365,10 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
         prompt = [tok.bos_token_id] + tok.encode(text)
         rid, created = f"chatcmpl-{uuid.uuid4().hex[:24]}", int(time.time())
         thinking = chat_encoding.normalize_effort(effort) is not None
-        aq = run_request(prompt, params)
+        if body.get("stream") and params.n != 1:
+            raise HTTPException(400, "streaming serves one completion per request")
+        qs = [run_request(prompt, c) for c in copies(params)]
+        aq = qs[0]
         if body.get("stream"):
             async def gen():
                 finish = None
@@ -376,22 +385,26 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
                     yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(guard(gen(), aq), media_type="text/event-stream")
-        ids, finish, lps = await collect(aq)
-        out_text = cut_at_stop(tok.decode(ids), params.stop, params.include_stop_str_in_output)[0]
-        msg = {"role": "assistant", "content": out_text}
-        if reasoning_parser or tool_call_parser:
-            try:
-                msg = chat_encoding.parse_completion(out_text, thinking=thinking and bool(reasoning_parser))
-                if not tool_call_parser and msg.get("tool_calls"):
-                    msg = {"role": "assistant", "content": out_text}
-            except ValueError:
-                pass        # a free-form completion (random-init models): returned as content
+        choices, n_out = [], 0
+        for j, q in enumerate(qs):
+            ids, finish, lps = await collect(q)
+            n_out += len(ids)
+            out_text = cut_at_stop(tok.decode(ids), params.stop, params.include_stop_str_in_output)[0]
+            msg = {"role": "assistant", "content": out_text}
+            if reasoning_parser or tool_call_parser:
+                try:
+                    msg = chat_encoding.parse_completion(out_text, thinking=thinking and bool(reasoning_parser))
+                    if not tool_call_parser and msg.get("tool_calls"):
+                        msg = {"role": "assistant", "content": out_text}
+                except ValueError:
+                    pass        # a free-form completion (random-init models): returned as content
+            choices.append({"index": j, "message": msg, "finish_reason": finish,
+                            "logprobs": chat_logprobs(ids, lps, params.logprobs)
+                            if params.logprobs is not None else None})
         return JSONResponse({"id": rid, "object": "chat.completion", "created": created, "model": name,
-                             "choices": [{"index": 0, "message": msg, "finish_reason": finish,
-                                          "logprobs": chat_logprobs(ids, lps, params.logprobs)
-                                          if params.logprobs is not None else None}],
-                             "usage": {"prompt_tokens": len(prompt), "completion_tokens": len(ids),
-                                       "total_tokens": len(prompt) + len(ids)}})
+                             "choices": choices,
+                             "usage": {"prompt_tokens": len(prompt), "completion_tokens": n_out,
+                                       "total_tokens": len(prompt) + n_out}})
 
     return app
 
