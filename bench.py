@@ -21,7 +21,7 @@ import os
 import sys
 import time
 
-BASELINE = {1: 161.0, 2: 210.0, 4: 214.0, 8: 214.0}   # BASELINE.md B1/B3/B5 (8 GPUs: the 4-GPU bar)
+BASELINE = {1: 161.0, 2: 210.0, 4: 214.0, 8: 214.0}   # published decode tok/s at 1 / 2 / 4 GPUs (8 GPUs: the 4-GPU bar)
 METRIC = "decode tok/s @1/32 streams + 8k prefill tok/s, DS4-Flash shape, 1/2/4/8 B200"
 
 
