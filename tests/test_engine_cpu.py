@@ -204,3 +204,22 @@ def test_n_completions_and_chat():
     c = llm.chat([{"role": "user", "content": "hi"}], SamplingParams(max_tokens=3, ignore_eos=True))
     assert len(c) == 1 and len(c[0].outputs[0].token_ids) == 3
     assert c[0].prompt_token_ids[0] == llm.tokenizer.bos_token_id
+
+
+def test_grow_state_moves_rows_to_a_larger_bucket():
+    import types
+    from vllm_moet_b200.engine.gpu_runner import DecodeState
+    from vllm_moet_b200.engine.llm import LLM
+    fake = types.SimpleNamespace(_states={}, _DecodeState=DecodeState, k=2, max_blocks=8, device="cpu")
+    fake._state = types.MethodType(LLM._state, fake)
+    st = fake._state(2)
+    st.tokens.copy_(torch.arange(6, dtype=torch.int32).view(2, 3))
+    st.seq_pos.copy_(torch.tensor([17, 40], dtype=torch.int32))
+    st.block_table[1, :3] = torch.tensor([5, 6, 7], dtype=torch.int32)
+    big = fake._state(4)
+    big.tokens.fill_(99)                          # stale rows of an earlier use of the bucket
+    st2 = LLM._grow_state(fake, st, 4)
+    assert st2 is big and st2.B == 4
+    assert torch.equal(st2.tokens[:2], st.tokens) and (st2.tokens[2:] == 0).all()
+    assert st2.seq_pos.tolist() == [17, 40, 0, 0] and st2.block_table[1, :3].tolist() == [5, 6, 7]
+    assert [LLM._bucket(n) for n in (1, 2, 3, 5, 32)] == [1, 2, 4, 8, 32]

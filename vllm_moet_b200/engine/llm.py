@@ -525,11 +525,28 @@ class LLM:
             self._states[B] = st
         return st
 
+    def _grow_state(self, st, B_new: int):
+        """Serving: move the running rows to the decode state of a larger graph bucket (rows
+        keep their index; KV caches are paged, so only tokens / positions / block tables move)."""
+        st2 = self._state(B_new)
+        n = st.B
+        for name in ("tokens", "seq_pos", "block_table"):
+            dst, src = getattr(st2, name), getattr(st, name)
+            dst.zero_()
+            dst[:n].copy_(src)
+        return st2
+
+    @staticmethod
+    def _bucket(n: int) -> int:
+        B = 1
+        while B < n:
+            B *= 2
+        return B
+
     def _run_native(self, reqs):
         runner = self.runner
-        B = 1
-        while B < min(len(reqs), self.ecfg.max_num_seqs):
-            B *= 2
+        B = self._bucket(min(len(reqs), self.ecfg.max_num_seqs))
+        cap = self._bucket(self.ecfg.max_num_seqs)
         st = self._state(B)
         kp1 = self.k + 1
         pin_active = torch.zeros(B, dtype=torch.int32, pin_memory=True)
@@ -542,10 +559,23 @@ class LLM:
         graph = runner.graphs.get(B) if self.ecfg.cuda_graphs else None
         bt_host = torch.zeros(B, self.max_blocks, dtype=torch.int32)
         while True:
-            self._poll(waiting, rows, sum(r is None for r in rows) - len(waiting),
-                       lambda r: self._finish_row(r, rows))
+            # serving: the batch may grow into a larger bucket, so offer room up to `cap` rows
+            room = (cap if self._between is not None else B) - sum(r is not None for r in rows) - len(waiting)
+            self._poll(waiting, rows, room, lambda r: self._finish_row(r, rows))
             if not (waiting or any(r is not None for r in rows)):
                 break
+            n_live = sum(r is not None for r in rows)
+            if self._between is not None and waiting and n_live >= B and B < cap:
+                B_new = min(cap, self._bucket(n_live + len(waiting)))
+                st = self._grow_state(st, B_new)
+                rows = rows + [None] * (B_new - B)
+                pin_active = torch.zeros(B_new, dtype=torch.int32, pin_memory=True)
+                pin_out = torch.zeros(B_new, kp1, dtype=torch.int32, pin_memory=True)
+                pin_acc = torch.zeros(B_new, dtype=torch.int32, pin_memory=True)
+                bt_new = torch.zeros(B_new, self.max_blocks, dtype=torch.int32)
+                bt_new[:B] = bt_host
+                bt_host, B = bt_new, B_new
+                graph = runner.graphs.get(B) if self.ecfg.cuda_graphs else None
             free = [i for i, r in enumerate(rows) if r is None]
             adm = []
             while waiting and free and self.blocks.can_allocate(len(waiting[0].prompt) + waiting[0].params.max_tokens + kp1 + 1):
