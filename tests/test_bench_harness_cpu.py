@@ -22,3 +22,46 @@ def test_tiny_recipe_run_lint_render(tmp_path):
     del bad["git_commit"]
     assert "missing field git_commit" in lint(bad, str(rec))
     json.dumps(res)
+
+
+def test_multi_rank_recipe_under_torchrun(tmp_path):
+    """A `parallel: {tp: 2}` recipe launched with torchrun (gloo on CPU): rank 0 writes one
+    result that lints; a multi-rank recipe started as one process is refused."""
+    import json
+    import os
+    import socket
+    import subprocess
+    import sys
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    out = tmp_path / "res"
+    env = dict(os.environ, MOET_SKIP_BUILD_CHECK="1")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(port), "-m", "vllm_moet_b200.bench", "run",
+                        "tiny_cpu_tp2", "--out", str(out)], capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stderr[-3000:]
+    files = list(out.iterdir())
+    assert len(files) == 1
+    from vllm_moet_b200.bench.harness import lint
+    res = json.loads(files[0].read_text())
+    assert lint(res) == [] and res["world"] == 2 and res["parallel"] == {"tp": 2}
+    assert any(x["probe"] == "coherence" and x["identical"] for x in res["results"])
+    r1 = subprocess.run([sys.executable, "-m", "vllm_moet_b200.bench", "run", "tiny_cpu_tp2", "--out", str(out)],
+                        capture_output=True, text=True, timeout=300, env=env)
+    assert r1.returncode != 0 and "needs tp * pp = 2 ranks" in (r1.stderr + r1.stdout)
+
+
+def test_every_recipe_is_well_formed():
+    import inspect
+    import os
+    import yaml
+    from vllm_moet_b200.bench.harness import RECIPE_DIR
+    from vllm_moet_b200.engine.llm import LLM
+    params = set(inspect.signature(LLM.__init__).parameters) - {"self", "model"}
+    for fn in sorted(os.listdir(RECIPE_DIR)):
+        rec = yaml.safe_load(open(os.path.join(RECIPE_DIR, fn)))
+        assert rec["name"] == fn[:-5], fn
+        assert set(rec.get("engine", {})) <= params | {"device"}, (fn, set(rec["engine"]) - params)
+        assert all(p["kind"] in ("decode", "prefill", "coherence") for p in rec["probes"]), fn
+        assert set(rec.get("parallel") or {}) <= {"tp", "pp", "ep"}, fn

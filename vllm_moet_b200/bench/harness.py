@@ -45,6 +45,36 @@ def _sync(dev):
         torch.cuda.synchronize()
 
 
+def _parallel(rec: dict) -> dict:
+    """Launch under torchrun for multi-rank recipes: `parallel: {tp, pp, ep}` -> LLM arguments.
+    Ranks are laid out stage-major (rank = stage * tp + tp_rank); every group is created on
+    every rank in the same order."""
+    par = rec.get("parallel") or {}
+    tp, pp, ep = int(par.get("tp", 1)), int(par.get("pp", 1)), bool(par.get("ep", False))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if tp * pp != world:
+        raise SystemExit(f"recipe {rec['name']} needs tp * pp = {tp * pp} ranks, launched with {world} "
+                         f"(torchrun --nproc-per-node {tp * pp} -m vllm_moet_b200.bench run ...)")
+    if world == 1:
+        return {}
+    import torch.distributed as dist
+    rank = int(os.environ.get("RANK", "0"))
+    cuda = torch.cuda.is_available() and rec.get("engine", {}).get("device", "cuda") != "cpu"
+    if cuda:
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    if not dist.is_initialized():
+        dist.init_process_group("nccl" if cuda else "gloo")
+    stage, tr = divmod(rank, tp)
+    tp_groups = [dist.new_group([s * tp + t for t in range(tp)]) for s in range(pp)] if tp > 1 else None
+    pp_groups = [dist.new_group([s * tp + t for s in range(pp)]) for t in range(tp)] if pp > 1 else None
+    kw = {}
+    if tp > 1:
+        kw.update(tensor_parallel_size=tp, tp_group=tp_groups[stage], tp_rank=tr, expert_parallel=ep)
+    if pp > 1:
+        kw.update(pipeline_parallel_size=pp, pp_group=pp_groups[tr], pp_rank=stage)
+    return kw
+
+
 def run_recipe(path: str) -> dict:
     from ..engine.llm import LLM
     from ..engine.sampling_params import SamplingParams
@@ -52,7 +82,8 @@ def run_recipe(path: str) -> dict:
     with open(path) as f:
         rec = yaml.safe_load(f)
     eng = dict(rec.get("engine", {}))
-    llm = LLM(rec["model"], **eng, **rec.get("overrides", {}))
+    par = _parallel(rec)
+    llm = LLM(rec["model"], **eng, **par, **rec.get("overrides", {}))
     g = torch.Generator().manual_seed(0)
     V = llm.cfg.vocab
 
@@ -92,6 +123,7 @@ def run_recipe(path: str) -> dict:
     dev = torch.cuda.get_device_name(0) if torch.cuda.is_available() and llm.device.type == "cuda" else "cpu"
     return {"schema": SCHEMA, "recipe": rec["name"], "recipe_sha256": file_sha(path), "git_commit": git_commit(),
             "source_fingerprint": source_fingerprint(), "device": dev, "results": results,
+            "world": int(os.environ.get("WORLD_SIZE", "1")), "parallel": rec.get("parallel") or {},
             "time": time.strftime("%Y-%m-%dT%H:%M:%SZ", time.gmtime())}
 
 
@@ -138,11 +170,12 @@ def main(argv=None):
     if a.cmd == "run":
         path = resolve_recipe(a.recipe)
         res = run_recipe(path)
-        os.makedirs(a.out, exist_ok=True)
-        out = os.path.join(a.out, f"{res['recipe']}.{int(time.time())}.json")
-        with open(out, "w") as f:
-            json.dump(res, f, indent=1)
-        print(out)
+        if int(os.environ.get("RANK", "0")) == 0:
+            os.makedirs(a.out, exist_ok=True)
+            out = os.path.join(a.out, f"{res['recipe']}.{int(time.time())}.json")
+            with open(out, "w") as f:
+                json.dump(res, f, indent=1)
+            print(out)
     elif a.cmd == "lint":
         bad = 0
         for fn in a.files:
