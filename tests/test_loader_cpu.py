@@ -207,3 +207,22 @@ def test_checkpoint_tokenizer_is_used(tmp_path):
     out = llm.generate(["w5 w7 w9"], SamplingParams(max_tokens=4, ignore_eos=True))[0]
     assert out.prompt_token_ids == [0, 8, 10, 12]
     assert out.outputs[0].text == llm.tokenizer.decode(out.outputs[0].token_ids)
+
+
+def test_nvfp4_dense_linear_roundtrip_and_loader(tmp_path):
+    from vllm_moet_b200.models.weights import Nvfp4Linear, make_linear
+    g = torch.Generator().manual_seed(3)
+    w = torch.randn(64, 128, generator=g) * 0.05
+    lin = make_linear(w, "nvfp4")
+    assert isinstance(lin, Nvfp4Linear) and lin.shape == (64, 128)
+    packed, sf, t2 = codebook.f32_to_nvfp4(w)
+    ref = codebook.E2M1_VALUES[codebook.split_packed_e2m1(packed).long()].float() * \
+        sf.float().repeat_interleave(16, 1) * t2
+    assert torch.equal(lin.dequant(), ref) and float((lin.dequant() - w).abs().max()) < 0.05
+    # the loader keeps NVFP4 dense tensors as they are when the model's dense format is NVFP4
+    from safetensors.torch import save_file
+    save_file({"x.weight": packed, "x.weight_scale": sf, "x.weight_scale_2": t2}, str(tmp_path / "m.safetensors"))
+    rd = CheckpointReader(str(tmp_path))
+    got = rd.linear("x", "nvfp4")
+    assert isinstance(got, Nvfp4Linear) and torch.equal(got.dequant(), ref)
+    assert torch.equal(rd.dense64("x").float(), ref)

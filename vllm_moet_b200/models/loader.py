@@ -43,7 +43,9 @@ def hf_config(path: str, **overrides) -> ModelConfig:
     with open(os.path.join(path, "config.json")) as f:
         c = json.load(f)
     qc = c.get("quantization_config") or {}
-    dense = "fp8" if qc.get("quant_method") == "fp8" or qc.get("fmt") == "e4m3" else "bf16"
+    algo = str(qc.get("quant_algo", "") or qc.get("quant_method", "")).lower()
+    dense = ("fp8" if qc.get("quant_method") == "fp8" or qc.get("fmt") == "e4m3" else
+             "nvfp4" if "nvfp4" in algo or "modelopt" in algo else "bf16")
     kw = dict(
         name=c.get("model_type", os.path.basename(os.path.normpath(path))),
         num_layers=c["num_hidden_layers"], hidden=c["hidden_size"], vocab=c["vocab_size"],
@@ -109,7 +111,14 @@ class CheckpointReader:
         return w.double()
 
     def linear(self, prefix: str, dtype: str, rows=None, cols=None):
-        """A dense linear, optionally sliced (rows / cols = (lo, hi))."""
+        """A dense linear, optionally sliced (rows / cols = (lo, hi)).  NVFP4 tensors stay
+        NVFP4 (bit-exact) when the model's dense format is nvfp4 and nothing is sliced."""
+        if dtype == "nvfp4" and rows is None and cols is None and self.has(prefix + ".weight_scale") \
+                and self.get(prefix + ".weight").dtype == torch.uint8:
+            from .weights import Nvfp4Linear
+            s2 = self.get(prefix + ".weight_scale_2") if self.has(prefix + ".weight_scale_2") else torch.tensor(1.0)
+            return Nvfp4Linear(self.get(prefix + ".weight").contiguous(), self.get(prefix + ".weight_scale"),
+                               s2.float().reshape(()))
         if dtype == "fp8" and rows is None and cols is None and self.has(prefix + ".weight_scale_inv"):
             s = self.get(prefix + ".weight_scale_inv").float()
             e = torch.log2(s)

@@ -1,6 +1,7 @@
 """Model weights: containers, expert slot layout, and synthetic random init.
 
 Dense stack: FP8 e4m3 with UE8M0 128x128 block scales (:class:`Fp8Linear`),
+NVFP4 (:class:`Nvfp4Linear`, the GLM dense format; the GPU runner serves it as FP8),
 or plain float for the CPU tiny model.  Routed experts: one slot per expert
 holding ``[codes13 | sc13 | codes2 | sc2]`` -- the fragment-major 2-bit
 planes of the fused gate/up matrix [2I, H] and of the down matrix [H, I]
@@ -64,9 +65,36 @@ class FloatLinear:
         return FloatLinear(self.w.to(device))
 
 
+@dataclass
+class Nvfp4Linear:
+    """y = x W^T with W [N, K] in NVFP4: packed e2m1 pairs [N, K/2] (low nibble = even k),
+    e4m3 block-16 scales [N, K/16] and an f32 tensor scale (the GLM dense format)."""
+    w: torch.Tensor
+    s: torch.Tensor
+    s2: torch.Tensor
+
+    @property
+    def shape(self):
+        return (self.w.shape[0], self.w.shape[1] * 2)
+
+    @classmethod
+    def from_float(cls, w: torch.Tensor) -> "Nvfp4Linear":
+        packed, sf, t2 = codebook.f32_to_nvfp4(w.float().cpu())
+        return cls(packed.to(w.device), sf.to(w.device), t2.to(w.device))
+
+    def dequant(self) -> torch.Tensor:
+        vals = codebook.E2M1_VALUES.to(self.w.device)[codebook.split_packed_e2m1(self.w).long()].float()
+        return vals * self.s.float().repeat_interleave(16, dim=1) * self.s2.float()
+
+    def to(self, device) -> "Nvfp4Linear":
+        return Nvfp4Linear(self.w.to(device), self.s.to(device), self.s2.to(device))
+
+
 def make_linear(w: torch.Tensor, dtype: str):
     if dtype == "fp8":
         return Fp8Linear.from_float(w)
+    if dtype == "nvfp4" and w.shape[-1] % 16 == 0:
+        return Nvfp4Linear.from_float(w)
     return FloatLinear(w.float())
 
 
