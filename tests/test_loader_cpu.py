@@ -226,3 +226,14 @@ def test_nvfp4_dense_linear_roundtrip_and_loader(tmp_path):
     got = rd.linear("x", "nvfp4")
     assert isinstance(got, Nvfp4Linear) and torch.equal(got.dequant(), ref)
     assert torch.equal(rd.dense64("x").float(), ref)
+
+
+def test_loader_refuses_layouts_it_cannot_represent(tmp_path):
+    T, _ = _make_ckpt(str(tmp_path), quant=False, shards=1)
+    from safetensors.torch import save_file
+    save_file({"model.layers.0.hc_pre_fn": torch.zeros(4)}, str(tmp_path / "extra.safetensors"))
+    idx = json.load(open(tmp_path / "model.safetensors.index.json"))
+    idx["weight_map"]["model.layers.0.hc_pre_fn"] = "extra.safetensors"
+    json.dump(idx, open(tmp_path / "model.safetensors.index.json", "w"))
+    with pytest.raises(NotImplementedError, match="hyper-connection"):
+        load_weights(str(tmp_path))

@@ -248,6 +248,11 @@ def load_weights(path: str, cfg: Optional[ModelConfig] = None, device="cpu", tp_
         cfg = cfg.replace(expert_scale="ue8m0")
     dev = torch.device(device)
     rd = CheckpointReader(path)
+    unsupported = [n for n in rd.where if ".hc_" in n or n.startswith("hc_") or ".hc_head" in n]
+    if unsupported:
+        raise NotImplementedError(f"hyper-connection (mHC) tensors such as {unsupported[0]!r}: this engine's layers "
+                                  "have single residual streams, so the checkpoint would be served as a different "
+                                  "model")
     H = cfg.hidden
     L = cfg.num_layers if num_layers is None else num_layers
     l0, l1 = pp_layer_range(L, pp_rank, pp_size)
