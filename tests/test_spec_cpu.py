@@ -137,3 +137,35 @@ def test_engine_first_token_distribution():
     for i in top.indices.tolist():
         sd = math.sqrt(float(want[i]) * (1 - float(want[i])) / n) + 1e-3
         assert abs(float(freq[i]) - float(want[i])) < 5 * sd, (i, float(freq[i]), float(want[i]))
+
+
+def test_dspark_engine_verifies_blocks():
+    """DSpark in the engine: whatever the drafter proposes, the output is the target's
+    greedy sequence; an oracle drafter (the true continuation, confident) gets every
+    allotted draft accepted and needs far fewer steps."""
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    from vllm_moet_b200.models import reference
+    p, n = [5, 6, 7, 8, 9], 12
+    rnd = LLM("tiny-moe", device="cpu", num_speculative_tokens=0, max_model_len=256, speculative_method="dspark",
+              dspark={"block": 4, "tau": 0.0, "budget_frac": 1.0})
+    want = reference.greedy_generate(rnd.mw, p, n)
+    assert rnd.generate([p], SamplingParams(max_tokens=n, ignore_eos=True))[0].outputs[0].token_ids == want
+    full = p + want
+
+    class Oracle:
+        def __init__(self, runner):
+            self.runner = runner
+
+        def propose(self, h, last):
+            (st,) = self.runner.rows.values()
+            nxt = full[st["pos"] + 1: st["pos"] + 5]
+            nxt = nxt + [0] * (4 - len(nxt))
+            R = h.shape[0]
+            return torch.tensor([nxt] * R), None, torch.ones(R, 4)
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=0, max_model_len=256, speculative_method="dspark",
+              dspark={"block": 4, "tau": 0.5, "budget_frac": 1.0})
+    llm.runner.dspark["drafter"] = Oracle(llm.runner)
+    out = llm.generate([p], SamplingParams(max_tokens=n, ignore_eos=True))[0].outputs[0].token_ids
+    assert out == want
+    assert llm.stats["accepted"] >= n - 4 and llm.stats["steps"] <= n // 5 + 2

@@ -52,7 +52,8 @@ class LLM:
                  pipeline_parallel_size: int = 1, pp_group=None, pp_rank: int = 0, expert_cache_slots: int = 0,
                  delta_slots: int = 0, gate: Optional[bool] = None, expert_parallel: bool = False,
                  expert_store: str = "pinned", expert_store_dir: Optional[str] = None, sp_group=None,
-                 dcp_group=None, dcp_interleave: int = 1, ep_group=None, **model_overrides):
+                 dcp_group=None, dcp_interleave: int = 1, ep_group=None, speculative_method: str = "mtp",
+                 dspark: Optional[dict] = None, **model_overrides):
         from ..models.loader import hf_config, is_checkpoint_dir, load_weights
         ckpt = model if is_checkpoint_dir(model) else None
         if ckpt is not None:
@@ -76,6 +77,10 @@ class LLM:
             raise NotImplementedError("SP prefill / DCP decode / DP+EP run on the CPU engine; the GPU runner has "
                                       "none of them yet")
         self._ep_group = ep_group
+        if speculative_method not in ("mtp", "dspark"):
+            raise ValueError(f"speculative_method {speculative_method!r}: mtp | dspark")
+        if speculative_method == "dspark" and self.device.type == "cuda":
+            raise NotImplementedError("DSpark block drafting runs on the CPU engine; the GPU runner drafts with MTP")
         if self.device.type == "cuda" and cfg.expert_scale != "ue8m0":
             cfg = cfg.replace(expert_scale="ue8m0")
         if self.device.type == "cuda" and cfg.dense_dtype != "fp8":
@@ -155,7 +160,8 @@ class LLM:
                 ep_partition(self.mw, dist.get_rank(ep_group), dist.get_world_size(ep_group))
             self.runner = TorchRunner(self.mw, self.k, max_model_len, self.device, tp_group=tp_group,
                                       sp_group=sp_group, dcp_group=dcp_group, dcp_interleave=dcp_interleave,
-                                      ep_group=ep_group)
+                                      ep_group=ep_group,
+                                      dspark=(dspark or {}) if speculative_method == "dspark" else None)
 
     def _attach_tracing(self):
         """Prefill span timers, routing capture, delta trace / dump and the gate JSONL

@@ -4,6 +4,8 @@ fp32 reference model and per-sequence KV lists.  Used for the CPU engine
 path and as the oracle of the GPU engine."""
 from __future__ import annotations
 
+from typing import Optional
+
 import torch
 
 from ..models import reference as ref
@@ -12,9 +14,16 @@ from ..models.weights import ModelWeights
 
 class TorchRunner:
     def __init__(self, mw: ModelWeights, k: int, max_len: int, device="cpu", tp_group=None, sp_group=None,
-                 dcp_group=None, dcp_interleave: int = 1, ep_group=None):
+                 dcp_group=None, dcp_interleave: int = 1, ep_group=None, dspark: Optional[dict] = None):
         self.mw = mw
-        self.k = k if mw.mtp is not None else 0
+        self.k = k if mw.mtp is not None and dspark is None else 0
+        self.dspark = None              # DSpark block drafting instead of MTP: {drafter, tau, budget_frac}
+        if dspark is not None:
+            from ..spec.dspark import DSparkDrafter
+            torch.manual_seed(dspark.get("seed", 0))
+            self.dspark = dict(drafter=dspark.get("drafter") or DSparkDrafter(mw.cfg.hidden, mw.cfg.vocab,
+                                                                               block=dspark.get("block", 4)),
+                               tau=dspark.get("tau", 0.5), budget_frac=dspark.get("budget_frac", 0.5))
         self.dev = torch.device(device)
         self.cs = ref.rope_cos_sin(mw.cfg, max_len + 64, self.dev)
         self.rows = {}
@@ -91,7 +100,7 @@ class TorchRunner:
                     ml, h = ref.mtp_forward(self.mw, h, torch.tensor([d], device=self.dev),
                                             torch.tensor([n + j - 1], device=self.dev), self.cs, mtp)
                     d = int(ml[-1].argmax()); drafts.append(d)
-            self.rows[r] = dict(main=main, mtp=mtp, tokens=[tgt] + drafts, pos=n, sample=smp)
+            self.rows[r] = dict(main=main, mtp=mtp, tokens=[tgt] + drafts, pos=n, sample=smp, hid=hid[-1])
             firsts.append(tgt)
         return firsts
 
@@ -101,7 +110,38 @@ class TorchRunner:
         with self._ctx():
             return self._step(rows)
 
+    def _dspark_step(self, rows):
+        """DSpark: one parallel block proposal per live row, widths from the batch-wide
+        verify budget (`allocate_widths`), then each row verifies [pending token] +
+        drafts[:width] in one target pass and emits the accepted prefix + the correction."""
+        from ..spec.dspark import allocate_widths
+        ds = self.dspark
+        drafter = ds["drafter"]
+        h = torch.stack([self.rows[r]["hid"].float() for r in rows])
+        last = torch.tensor([self.rows[r]["tokens"][0] for r in rows], device=self.dev)
+        drafts, _, surv = drafter.propose(h, last)
+        L = drafts.shape[1]
+        widths = allocate_widths(surv, torch.ones(L), len(rows), L, ds["tau"], ds["budget_frac"])
+        out = {}
+        for i, r in enumerate(rows):
+            st = self.rows[r]
+            p, w = st["pos"], int(widths[i])
+            st["main"].truncate(p)
+            toks = torch.tensor([st["tokens"][0]] + drafts[i, :w].tolist(), device=self.dev)
+            logits, hid = ref.forward(self.mw, toks, torch.arange(p, p + w + 1, device=self.dev), self.cs,
+                                      st["main"])
+            tg = logits.argmax(-1).tolist()
+            a = 0
+            while a < w and int(drafts[i, a]) == tg[a]:
+                a += 1
+            self.last_logits[r] = logits[: a + 1]
+            st["tokens"], st["pos"], st["hid"] = [tg[a]], p + a + 1, hid[a]
+            out[r] = (tg[: a + 1], a)
+        return out
+
     def _step(self, rows):
+        if self.dspark is not None:
+            return self._dspark_step(rows)
         out = {}
         k = self.k
         for r in rows:
