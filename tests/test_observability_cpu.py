@@ -38,3 +38,16 @@ def test_span_timers_cpu():
     with t.span("prefill"):
         sum(range(1000))
     assert t.summary()["prefill"]["n"] == 1
+
+
+def test_decode_roofline_model():
+    from vllm_moet_b200.config import ds4_flash_config
+    from vllm_moet_b200.utils.roofline import roofline, step_bytes
+    cfg = ds4_flash_config()
+    one = step_bytes(cfg, streams=1)
+    many = step_bytes(cfg, streams=32)
+    assert 20 < one["experts_distinct_per_layer"] < 24 and 230 < many["experts_distinct_per_layer"] <= 256
+    assert many["experts"] > 9 * one["experts"] and many["dense"] == one["dense"]
+    assert abs(step_bytes(cfg, streams=1, tp=2)["lm_head"] * 2 - one["lm_head"]) < 1
+    r = roofline(cfg, 6549.1, streams=1, measured_ms=6.17)
+    assert 1.0 < r["floor_ms"] < 1.3 and 0.15 < r["fraction_of_roofline"] < 0.25
