@@ -65,3 +65,43 @@ def test_every_recipe_is_well_formed():
         assert set(rec.get("engine", {})) <= params | {"device"}, (fn, set(rec["engine"]) - params)
         assert all(p["kind"] in ("decode", "prefill", "coherence") for p in rec["probes"]), fn
         assert set(rec.get("parallel") or {}) <= {"tp", "pp", "ep"}, fn
+
+
+def test_recipe_probes_over_http(tmp_path):
+    """`bench run <recipe> --url ...`: the same probes against a running server."""
+    import json
+    import socket
+    import threading
+    import time
+    import requests
+    import uvicorn
+    from vllm_moet_b200.bench.harness import lint, main
+    from vllm_moet_b200.engine.llm import LLM
+    from vllm_moet_b200.entrypoints.openai_server import EngineWorker, build_app
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256, max_num_seqs=4)
+    w = EngineWorker(llm, "tiny-moe")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    srv = uvicorn.Server(uvicorn.Config(build_app(w), host="127.0.0.1", port=port, log_level="warning"))
+    th = threading.Thread(target=srv.run, daemon=True)
+    th.start()
+    url = f"http://127.0.0.1:{port}"
+    try:
+        for _ in range(100):
+            try:
+                if requests.get(url + "/health", timeout=1).ok:
+                    break
+            except requests.ConnectionError:
+                time.sleep(0.1)
+        main(["run", "tiny_cpu", "--out", str(tmp_path), "--url", url])
+        (f,) = list(tmp_path.iterdir())
+        res = json.loads(f.read_text())
+        assert lint(res) == [] and res["mode"] == "http"
+        dec = [r for r in res["results"] if r["probe"] == "decode"]
+        assert [r["streams"] for r in dec] == [1, 4] and all(r["tok_s"] > 0 for r in dec)
+        assert any(r["probe"] == "coherence" and r["identical"] for r in res["results"])
+    finally:
+        srv.should_exit = True
+        th.join(timeout=10)
+        w.close()

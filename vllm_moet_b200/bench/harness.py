@@ -75,6 +75,62 @@ def _parallel(rec: dict) -> dict:
     return kw
 
 
+def run_recipe_http(path: str, url: str) -> dict:
+    """The recipe's probes against a running OpenAI-compatible server (`serve` mode):
+    decode = concurrent streams of /v1/completions (wall-clock tok/s), prefill = one
+    request with max_tokens 1 (prompt tok/s, i.e. time to first token), coherence = the
+    same greedy request twice."""
+    import concurrent.futures as cf
+    import requests
+    from ..ops.fingerprint import source_fingerprint
+    with open(path) as f:
+        rec = yaml.safe_load(f)
+    url = url.rstrip("/")
+    info = requests.get(url + "/v1/models", timeout=30).json()["data"][0]
+    V = int(rec.get("vocab") or 259)            # token ids 3..V-1 exist in every preset (byte range)
+    g = torch.Generator().manual_seed(0)
+
+    def prompt(n):
+        return torch.randint(3, V, (n,), generator=g).tolist()
+
+    def complete(p, n):
+        r = requests.post(url + "/v1/completions", json={"prompt": p, "max_tokens": n, "ignore_eos": True},
+                          timeout=3600)
+        r.raise_for_status()
+        return r.json()["choices"][0]["token_ids"]
+    results: List[dict] = []
+    for pr in rec.get("probes", []):
+        kind = pr["kind"]
+        if kind == "decode":
+            for S in pr["streams"]:
+                ps = [prompt(pr["prompt_len"]) for _ in range(S)]
+                with cf.ThreadPoolExecutor(S) as ex:
+                    list(ex.map(lambda p: complete(p, 2), ps))              # warm
+                    t0 = time.perf_counter()
+                    outs = list(ex.map(lambda p: complete(p, pr["tokens"]), ps))
+                    dt = time.perf_counter() - t0
+                results.append({"probe": "decode", "streams": S, "tok_s": sum(map(len, outs)) / dt,
+                                "wall_s": dt})
+        elif kind == "prefill":
+            for n in pr["lengths"]:
+                p = prompt(n)
+                complete(p, 1)
+                t0 = time.perf_counter()
+                complete(p, 1)
+                dt = time.perf_counter() - t0
+                results.append({"probe": "prefill", "length": n, "tok_s": n / dt, "ms": dt * 1e3})
+        elif kind == "coherence":
+            p = prompt(pr["prompt_len"])
+            a, b = complete(p, pr["tokens"]), complete(p, pr["tokens"])
+            results.append({"probe": "coherence", "identical": a == b, "tokens": len(a)})
+        else:
+            raise ValueError(f"unknown probe kind {kind!r}")
+    return {"schema": SCHEMA, "recipe": rec["name"], "recipe_sha256": file_sha(path), "git_commit": git_commit(),
+            "source_fingerprint": source_fingerprint(), "device": f"http {url} ({info['id']})", "results": results,
+            "world": 1, "parallel": rec.get("parallel") or {}, "mode": "http",
+            "time": time.strftime("%Y-%m-%dT%H:%M:%SZ", time.gmtime())}
+
+
 def run_recipe(path: str) -> dict:
     from ..engine.llm import LLM
     from ..engine.sampling_params import SamplingParams
@@ -164,12 +220,13 @@ def main(argv=None):
     ap = argparse.ArgumentParser(prog="python -m vllm_moet_b200.bench")
     sub = ap.add_subparsers(dest="cmd", required=True)
     r = sub.add_parser("run"); r.add_argument("recipe"); r.add_argument("--out", default="bench_results")
+    r.add_argument("--url", default=None, help="run the probes against a running server instead of in-process")
     li = sub.add_parser("lint"); li.add_argument("files", nargs="+")
     rn = sub.add_parser("render"); rn.add_argument("files", nargs="+")
     a = ap.parse_args(argv)
     if a.cmd == "run":
         path = resolve_recipe(a.recipe)
-        res = run_recipe(path)
+        res = run_recipe_http(path, a.url) if a.url else run_recipe(path)
         if int(os.environ.get("RANK", "0")) == 0:
             os.makedirs(a.out, exist_ok=True)
             out = os.path.join(a.out, f"{res['recipe']}.{int(time.time())}.json")
