@@ -51,3 +51,23 @@ def test_decode_roofline_model():
     assert abs(step_bytes(cfg, streams=1, tp=2)["lm_head"] * 2 - one["lm_head"]) < 1
     r = roofline(cfg, 6549.1, streams=1, measured_ms=6.17)
     assert 1.0 < r["floor_ms"] < 1.3 and 0.15 < r["fraction_of_roofline"] < 0.25
+
+
+def test_delta_policy_simulator(tmp_path):
+    import numpy as np
+    from vllm_moet_b200.tools.delta_sim import main, simulate
+    rng = np.random.default_rng(0)
+    steps, L, rows, E = 200, 3, 6, 32
+    # a hot set of 4 experts per layer gets 80 % of the routing, the rest is uniform noise
+    hot = rng.integers(0, E, (L, 4))
+    routes = np.where(rng.random((steps, L, rows)) < 0.8, hot[None, :, rng.integers(0, 4, rows)].squeeze(),
+                      rng.integers(0, E, (steps, L, rows))).astype(np.int32)
+    routes[:, :, -1] = -1                                    # padding rows are ignored
+    big = simulate(routes, slots=L * E, policy="lru")
+    assert big["evictions_per_step"] == 0 and big["hit_rate_distinct"] > 0.9
+    small_lru = simulate(routes, slots=16, policy="lru")
+    small_freq = simulate(routes, slots=16, policy="freq")
+    assert small_freq["hit_rate_tokens"] >= small_lru["hit_rate_tokens"] - 0.02   # frequency keeps the hot set
+    assert 0 < small_freq["hit_rate_tokens"] <= 1 and small_lru["evictions_per_step"] > 0
+    np.save(tmp_path / "r.npy", routes)
+    main([str(tmp_path / "r.npy"), "--slots", "16", "--policy", "lru"])
