@@ -263,3 +263,13 @@ def test_n_choices_over_http(server):
                          timeout=120).json()
     assert len(chat["choices"]) == 2 and chat["usage"]["completion_tokens"] == 6
     assert requests.post(url + "/v1/completions", json=dict(body, stream=True), timeout=120).status_code == 400
+
+
+def test_tokenize_detokenize_version(server):
+    url, _ = server
+    t = requests.post(url + "/tokenize", json={"prompt": "hi"}).json()
+    assert t["tokens"][0] == 1 and t["count"] == 3
+    assert requests.post(url + "/detokenize", json={"tokens": t["tokens"][1:]}).json()["prompt"] == "hi"
+    c = requests.post(url + "/tokenize", json={"messages": [{"role": "user", "content": "hi"}]}).json()
+    assert c["count"] > 3
+    assert requests.get(url + "/version").json()["version"]

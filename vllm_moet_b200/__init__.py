@@ -2,6 +2,8 @@
 codebook experts, MLA attention and MTP speculative decoding."""
 import torch  # noqa: F401  (loads libc10 before the native extension)
 
+__version__ = "0.1.0"
+
 from .config import EngineConfig, ModelConfig, MoetConfig, ParallelConfig, get_preset  # noqa: F401
 from .engine.sampling_params import RequestOutput, SamplingParams  # noqa: F401
 

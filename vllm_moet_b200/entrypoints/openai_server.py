@@ -283,6 +283,26 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
         return {"object": "list", "data": [{"id": name, "object": "model", "owned_by": "vllm_moet_b200",
                                             "max_model_len": worker.llm.ecfg.max_model_len}]}
 
+    @app.post("/tokenize")
+    async def tokenize(body: Dict[str, Any]):
+        if "messages" in body:
+            text = chat_encoding.render(body["messages"], tools=body.get("tools"),
+                                        reasoning_effort=body.get("reasoning_effort", "none"))
+            ids = [tok.bos_token_id] + tok.encode(text)
+        else:
+            ids = _prompt_ids(body.get("prompt", "")) if body.get("add_special_tokens", True) \
+                else tok.encode(body.get("prompt", ""))
+        return {"tokens": ids, "count": len(ids), "max_model_len": worker.llm.ecfg.max_model_len}
+
+    @app.post("/detokenize")
+    async def detokenize(body: Dict[str, Any]):
+        return {"prompt": tok.decode(list(body.get("tokens", [])))}
+
+    @app.get("/version")
+    async def version():
+        from .. import __version__
+        return {"version": __version__}
+
     @app.get("/metrics")
     async def metrics():
         lines = [f"moet_{k}_total {v}" for k, v in worker.stats.items()]
