@@ -273,3 +273,33 @@ def test_tokenize_detokenize_version(server):
     c = requests.post(url + "/tokenize", json={"messages": [{"role": "user", "content": "hi"}]}).json()
     assert c["count"] > 3
     assert requests.get(url + "/version").json()["version"]
+
+
+def test_chat_stream_parser_splits_reasoning_content_and_tool_calls():
+    from vllm_moet_b200.entrypoints import chat_encoding as ce
+    from vllm_moet_b200.entrypoints.openai_server import _ChatParseStream
+    text = "let me think" + ce.THINK_END + "Sure." + ce.encode_tool_calls(
+        [{"function": {"name": "get_weather", "arguments": {"city": "Oslo"}}}]) + ce.EOS
+    for step in (1, 3, 7, len(text)):            # any chunking gives the same deltas
+        ps = _ChatParseStream(thinking=True, tools=True)
+        pieces = [text[i:i + step] for i in range(0, len(text), step)]
+        out = [ps.push(p, i == len(pieces) - 1) for i, p in enumerate(pieces)]
+        assert "".join(d.get("reasoning_content", "") for d in out) == "let me think"
+        assert "".join(d.get("content", "") for d in out) == "Sure."
+        calls = [c for d in out for c in d.get("tool_calls", [])]
+        assert len(calls) == 1 and calls[0]["function"]["name"] == "get_weather" and calls[0]["index"] == 0
+        assert json.loads(calls[0]["function"]["arguments"]) == {"city": "Oslo"}
+    plain = _ChatParseStream(thinking=False, tools=True)
+    d = [plain.push("no tools here", False), plain.push("", True)]
+    assert "".join(x.get("content", "") for x in d) == "no tools here" and plain.tool_calls is None
+
+
+def test_chat_stream_over_http(server):
+    url, _ = server
+    r = requests.post(url + "/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}],
+                                                          "max_tokens": 4, "ignore_eos": True, "stream": True},
+                      stream=True, timeout=120)
+    events = [json.loads(ln[6:]) for ln in r.iter_lines(decode_unicode=True)
+              if ln.startswith("data: ") and ln != "data: [DONE]"]
+    assert events[0]["choices"][0]["delta"]["role"] == "assistant"
+    assert events[-1]["choices"][0]["finish_reason"] == "length"

@@ -165,6 +165,60 @@ def _params_from(body: Dict[str, Any], default_max: int = 16) -> SamplingParams:
                           min_tokens=int(body.get("min_tokens") or 0), logprobs=lp, n=int(body.get("n") or 1))
 
 
+class _ChatParseStream:
+    """Incremental DS4 chat parsing for streamed chat completions: text before ``</think>``
+    goes out as ``reasoning_content`` deltas (thinking mode), then ``content`` deltas; a
+    tail that could still be the start of a marker is held back; from the DSML tool-call
+    block on, text is buffered and parsed at the end into one ``tool_calls`` delta."""
+
+    def __init__(self, thinking: bool, tools: bool):
+        self.mode = "reasoning_content" if thinking else "content"
+        self.thinking, self.tools = thinking, tools
+        self.buf, self.full, self.tool_buf = "", "", ""
+        self.tool_calls = None
+        self.call_start = f"\n\n<{chat_encoding.DSML}{chat_encoding.CALLS_BLOCK}>"
+
+    def _marker(self):
+        if self.mode == "reasoning_content":
+            return chat_encoding.THINK_END
+        return self.call_start if self.tools and self.mode == "content" else None
+
+    def push(self, text: str, finished: bool) -> Dict[str, Any]:
+        self.full += text
+        delta: Dict[str, Any] = {}
+
+        def emit(key, piece):
+            if piece:
+                delta[key] = delta.get(key, "") + piece
+        if self.mode == "tools":
+            self.tool_buf += text
+        else:
+            self.buf += text
+        while self.mode != "tools":
+            m = self._marker()
+            if m is not None and m in self.buf:
+                before, after = self.buf.split(m, 1)
+                emit(self.mode, before)
+                if self.mode == "reasoning_content":
+                    self.mode, self.buf = "content", after
+                else:
+                    self.mode, self.tool_buf, self.buf = "tools", m + after, ""
+                continue
+            hold = 0 if finished or m is None else len(m) - 1
+            cut = max(0, len(self.buf) - hold)
+            emit(self.mode, self.buf[:cut].replace(chat_encoding.EOS, "") if finished else self.buf[:cut])
+            self.buf = self.buf[cut:]
+            break
+        if finished and self.mode == "tools":
+            try:
+                msg = chat_encoding.parse_completion(self.full, thinking=self.thinking)
+                self.tool_calls = msg.get("tool_calls") or []
+                delta["tool_calls"] = [dict(c, index=i) for i, c in enumerate(self.tool_calls)]
+            except ValueError:
+                emit("content", self.tool_buf)          # not a valid tool-call block: plain text
+        return delta
+
+
 class _StopStream:
     """Incremental text for streaming with stop strings: a tail that could still be the
     start of a stop string is held back until it is resolved (as vLLM streams)."""
@@ -394,14 +448,18 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
                 finish = None
                 first = True
                 ss = _StopStream(tok, params)
+                cps = _ChatParseStream(thinking and bool(reasoning_parser), bool(tool_call_parser)) \
+                    if (reasoning_parser or tool_call_parser) else None
                 while finish is None:
                     ids, finish, _ = await aq.get()
-                    delta = {"content": ss.push(ids, finish is not None) if params.stop else tok.decode(ids)}
+                    text = ss.push(ids, finish is not None) if params.stop else tok.decode(ids)
+                    delta = cps.push(text, finish is not None) if cps is not None else {"content": text}
                     if first:
                         delta["role"] = "assistant"
                         first = False
+                    fr = "tool_calls" if finish and cps is not None and cps.tool_calls else finish
                     chunk = {"id": rid, "object": "chat.completion.chunk", "created": created, "model": name,
-                             "choices": [{"index": 0, "delta": delta, "finish_reason": finish}]}
+                             "choices": [{"index": 0, "delta": delta, "finish_reason": fr}]}
                     yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(guard(gen(), aq), media_type="text/event-stream")
