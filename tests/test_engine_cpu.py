@@ -223,3 +223,18 @@ def test_grow_state_moves_rows_to_a_larger_bucket():
     assert torch.equal(st2.tokens[:2], st.tokens) and (st2.tokens[2:] == 0).all()
     assert st2.seq_pos.tolist() == [17, 40, 0, 0] and st2.block_table[1, :3].tolist() == [5, 6, 7]
     assert [LLM._bucket(n) for n in (1, 2, 3, 5, 32)] == [1, 2, 4, 8, 32]
+
+
+def test_prompt_logprobs_match_reference():
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+    p = [5, 6, 7, 8, 9, 10]
+    o = llm.generate([p], SamplingParams(max_tokens=2, ignore_eos=True, prompt_logprobs=2))[0]
+    assert o.prompt_logprobs[0] is None and len(o.prompt_logprobs) == len(p)
+    lg, _ = reference.forward(llm.mw, torch.tensor(p), torch.arange(len(p)), reference.rope_cos_sin(llm.cfg, 64))
+    lp = torch.log_softmax(lg, -1)
+    for i in range(1, len(p)):
+        d = o.prompt_logprobs[i]
+        assert abs(d[p[i]] - float(lp[i - 1, p[i]])) < 1e-4 and len(d) <= 3
+    assert llm.generate([p], SamplingParams(max_tokens=2))[0].prompt_logprobs is None

@@ -40,6 +40,7 @@ class _Req:
     callback: Optional[object] = None     # callback(new_token_ids, finish_reason) for streaming
     text: Optional[str] = None            # final text when a stop string cut it
     logprobs: Optional[list] = None       # per emitted token {token: logprob} (when requested)
+    prompt_logprobs: Optional[list] = None
     stop_reason: Optional[object] = None
 
 
@@ -336,7 +337,8 @@ class LLM:
         for i, t in enumerate(toks):
             mine = [o for o, w in zip(outs, owner) if w == i]
             comps = [dataclasses.replace(o.outputs[0], index=j) for j, o in enumerate(mine)]
-            grouped.append(RequestOutput(mine[0].request_id, t, comps, metrics=mine[0].metrics))
+            grouped.append(RequestOutput(mine[0].request_id, t, comps, metrics=mine[0].metrics,
+                                         prompt_logprobs=mine[0].prompt_logprobs))
         return grouped
 
     def chat(self, messages, sampling_params: Optional[SamplingParams] = None, reasoning_effort: str = "none",
@@ -358,6 +360,8 @@ class LLM:
     def _check_request(self, t, sp):
         if sp.logprobs is not None and self.device.type == "cuda" and self._tp_group is not None:
             raise NotImplementedError("logprobs under tensor parallelism: each rank holds a vocab shard")
+        if sp.prompt_logprobs is not None and self.device.type == "cuda":
+            raise NotImplementedError("prompt_logprobs: the GPU prefill keeps only each prompt's last logits")
         if sp.temperature != 0 and self.device.type == "cuda":
             raise NotImplementedError("temperature > 0: the GPU runner verifies drafts greedily inside the "
                                       "decode graph; sampling is served by the CPU engine")
@@ -400,7 +404,8 @@ class LLM:
         return [RequestOutput(r.rid, r.prompt, [CompletionOutput(
                     0, r.text if r.text is not None else self.tokenizer.decode(r.out), r.out, r.finish, r.stop_reason,
                     r.logprobs, (sum(d[t] for d, t in zip(r.logprobs, r.out)) if r.logprobs is not None else None))],
-                              metrics=dict(ttft_s=r.t_first - r.t_arrive, e2e_s=r.t_done - r.t_arrive))
+                              metrics=dict(ttft_s=r.t_first - r.t_arrive, e2e_s=r.t_done - r.t_arrive),
+                              prompt_logprobs=r.prompt_logprobs)
                 for r in reqs]
 
     # ------------------------------------------------------------------ helpers
@@ -504,6 +509,11 @@ class LLM:
                 firsts = self.runner.prefill([r.prompt for r in adm], [r.row for r in adm], [r.params for r in adm])
                 for r, f in zip(adm, firsts):
                     r.t_first = time.perf_counter()
+                    pl = self.runner.prompt_logits.get(r.row)
+                    if r.params.prompt_logprobs is not None and pl is not None:
+                        from .sampling_params import logprob_entries
+                        r.prompt_logprobs = [None] + (logprob_entries(pl, r.prompt[1:], r.params.prompt_logprobs)
+                                                      if len(r.prompt) > 1 else [])
                     if self._emit(r, [f], self.runner.last_logits.get(r.row)):
                         rows[r.row] = None; self.runner.release(r.row)
             if ep is not None:

@@ -19,6 +19,7 @@ class SamplingParams:
     min_tokens: int = 0             # no stop condition before this many tokens
     logprobs: Optional[int] = None  # per generated token: the chosen token's and the top-N log-probabilities
     n: int = 1                      # completions per prompt (copies i > 0 sample with seed + i when seeded)
+    prompt_logprobs: Optional[int] = None   # per prompt token after the first: its and the top-N log-probabilities
 
     def __post_init__(self):
         if isinstance(self.stop, str):
@@ -73,6 +74,7 @@ class RequestOutput:
     outputs: List[CompletionOutput]
     finished: bool = True
     metrics: dict = field(default_factory=dict)
+    prompt_logprobs: Optional[List[Optional[Dict[int, float]]]] = None   # None for the first prompt token
 
 
 def logprob_entries(logits, tokens, top_n: int):

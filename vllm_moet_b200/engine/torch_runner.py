@@ -28,6 +28,7 @@ class TorchRunner:
         self.cs = ref.rope_cos_sin(mw.cfg, max_len + 64, self.dev)
         self.rows = {}
         self.last_logits = {}           # row -> logits rows that predicted the tokens emitted by the last call
+        self.prompt_logits = {}         # row -> logits of the prompt positions (prompt_logprobs)
         self.tp_group = tp_group        # tensor-parallel CPU ranks (gloo): sharded weights, all-reduced partials
         self.sp_group = sp_group        # sequence-parallel prefill ranks: prompt chunks, gathered MLA latents
         self.dcp_group = dcp_group      # decode-context-parallel ranks: KV interleaved by position, LSE merge
@@ -83,6 +84,7 @@ class TorchRunner:
             else:
                 logits, hid = ref.forward(self.mw, toks, torch.arange(n, device=self.dev), self.cs, main)
                 last = logits[-1]
+                self.prompt_logits[r] = logits[:-1]          # rows that predicted prompt tokens 1..n-1
             self.last_logits[r] = last[None]
             if smp is None:
                 tgt = int(last.argmax())
@@ -194,3 +196,4 @@ class TorchRunner:
     def release(self, r):
         self.rows.pop(r, None)
         self.last_logits.pop(r, None)
+        self.prompt_logits.pop(r, None)
