@@ -1,0 +1,181 @@
+"""The GPU engine's decode loop (`LLM._run_native`) on the CPU, with a fake native runner.
+
+The fake runner stands in for the CUDA kernels with a deterministic model: the token after
+`t` at position `p` is f(t, p).  Its decode step verifies the row's drafts against f the
+way the captured graph does (accepted drafts + one correction token, `n_acc`), and its
+drafts are right on most steps and wrong on some, so acceptance varies.  Whatever the
+batching, joins, aborts or bucket growth, every request must come out as the chain of f
+from its prompt.  Only the host loop is under test here; the kernels are tested on GPUs.
+"""
+import itertools
+import math
+import types
+
+import pytest
+import torch
+
+from vllm_moet_b200 import SamplingParams
+from vllm_moet_b200.config import EngineConfig, MoetConfig, tiny_config
+from vllm_moet_b200.engine.gpu_runner import DecodeState
+from vllm_moet_b200.engine.kv_manager import BlockManager
+from vllm_moet_b200.engine.llm import LLM
+from vllm_moet_b200.engine.tokenizer import ByteTokenizer
+
+V = 1024
+
+
+def f(t: int, p: int) -> int:
+    return (int(t) * 7 + int(p) * 3 + 11) % (V - 3) + 3
+
+
+def chain(prompt, n):
+    out, t, p = [], prompt[-1], len(prompt) - 1
+    for _ in range(n):
+        t = f(t, p)
+        out.append(t)
+        p += 1
+    return out
+
+
+class FakeRunner:
+    def __init__(self, k):
+        self.k, self.graphs, self.steps = k, {}, 0
+        self.ws_prefill = self
+        self.logits = {}
+
+    def _drafts(self, t, p):
+        d = []
+        for j in range(self.k):
+            t = f(t, p + j)
+            d.append(t)
+        if self.steps % 3 == 1 and d:          # a wrong draft now and then
+            d[-1] = (d[-1] + 1) % V
+        return d
+
+    def prefill(self, prompts, bts, rows, st):
+        firsts = []
+        for pr, r in zip(prompts, rows):
+            t0 = f(pr[-1], len(pr) - 1)
+            st.tokens[r] = torch.tensor([t0] + self._drafts(t0, len(pr)), dtype=torch.int32)
+            st.seq_pos[r] = len(pr)
+            firsts.append(t0)
+        self.prefill_logits = torch.stack([self._onehot(t) for t in firsts])
+        return torch.tensor(firsts)
+
+    def get(self, name, shape, dtype):                     # ws_prefill.get("main.logits", ...)
+        return self.prefill_logits
+
+    @staticmethod
+    def _onehot(t):
+        x = torch.zeros(V)
+        x[int(t)] = 10.0
+        return x
+
+    def decode_body(self, st):
+        self.steps += 1
+        kp1 = self.k + 1
+        lg = torch.zeros(st.B * kp1, V)
+        for r in range(st.B):
+            if not int(st.active[r]):
+                continue
+            toks, p = st.tokens[r].tolist(), int(st.seq_pos[r])
+            tg = [f(toks[j], p + j) for j in range(kp1)]
+            a = 0
+            while a < self.k and toks[a + 1] == tg[a]:
+                a += 1
+            st.out_tokens[r] = torch.tensor(tg, dtype=torch.int32)
+            st.n_acc[r] = a
+            for j in range(kp1):
+                lg[r * kp1 + j] = self._onehot(tg[j])
+            nxt = tg[a]
+            st.tokens[r] = torch.tensor([nxt] + self._drafts(nxt, p + a + 1), dtype=torch.int32)
+            st.seq_pos[r] = p + a + 1
+        self.logits[st.B] = lg
+
+    def main_logits(self, B):
+        return self.logits.get(B)
+
+    def route_ids(self, B):
+        return []
+
+    def check_status(self, where):
+        pass
+
+
+class _Stream:
+    def synchronize(self):
+        pass
+
+
+@pytest.fixture
+def engine(monkeypatch):
+    zeros = torch.zeros
+
+    def zeros_no_pin(*a, pin_memory=False, **kw):
+        return zeros(*a, **kw)
+    monkeypatch.setattr(torch, "zeros", zeros_no_pin)
+    monkeypatch.setattr(torch.cuda, "current_stream", lambda *a, **k: _Stream())
+
+    def make(max_num_seqs=4, k=2):
+        llm = object.__new__(LLM)
+        cfg = tiny_config()
+        llm.cfg, llm.k, llm.device = cfg, k, torch.device("cpu")
+        llm.ecfg = EngineConfig(model=cfg, moet=MoetConfig(), max_num_seqs=max_num_seqs, max_model_len=512,
+                                num_speculative_tokens=k, cuda_graphs=False)
+        llm.max_blocks = -(-(512 + k + 2) // 64)
+        llm.blocks = BlockManager(max_num_seqs * llm.max_blocks + 1)
+        llm.tokenizer = ByteTokenizer(V)
+        llm._states, llm._DecodeState, llm._ids = {}, DecodeState, itertools.count()
+        llm.cache = llm.delta = llm.gate = llm.routing = llm.timers = None
+        llm._tp_group = llm._pp_group = llm._ep_group = None
+        llm._decode_steps, llm.stats = 0, {}
+        llm.runner = FakeRunner(k)
+        llm._run_torch = types.MethodType(LLM._run_native, llm)    # generate() dispatches by device type
+        return llm
+    return make
+
+
+def test_batch_decodes_the_model_chain(engine):
+    llm = engine()
+    prompts = [[5, 6, 7], [40, 41], [9, 10, 11, 12]]
+    lens = [9, 4, 13]
+    out = llm.generate(prompts, [SamplingParams(max_tokens=n, ignore_eos=True) for n in lens])
+    for o, p, n in zip(out, prompts, lens):
+        assert o.outputs[0].token_ids == chain(p, n) and o.outputs[0].finish_reason == "length"
+    assert llm.stats["accepted"] > 0
+    assert llm.blocks.can_allocate(4 * 512 - 64)          # every request's blocks were released
+
+
+def test_joins_grow_the_bucket_and_aborts_free_rows(engine):
+    llm = engine(max_num_seqs=4)
+    ev = {}
+
+    def cb(name):
+        return lambda ids, fin, lp=None: ev.setdefault(name, []).append((list(ids), fin))
+    step = [0]
+    joined = {"j1": [20, 21], "j2": [30, 31, 32], "j3": [50]}
+
+    def between(n_free):
+        step[0] += 1
+        new = []
+        if step[0] == 2:                                  # three requests while the 1-row bucket is busy
+            new = [(rid, p, SamplingParams(max_tokens=40 if rid == "j2" else 6, ignore_eos=True), cb(rid))
+                   for rid, p in joined.items()]
+        return new[:max(0, n_free)], ({"j2"} if step[0] == 4 else set())
+    out = llm.generate([[5, 6, 7]], SamplingParams(max_tokens=14, ignore_eos=True), callbacks=[cb("a")],
+                       request_ids=["a"], between_steps=between)
+    assert out[0].outputs[0].token_ids == chain([5, 6, 7], 14)
+    assert 4 in llm._states                               # the batch moved into the 4-row bucket
+    for rid in ("j1", "j3"):
+        assert sum((ids for ids, _ in ev[rid]), []) == chain(joined[rid], 6) and ev[rid][-1][1] == "length"
+    got = sum((ids for ids, _ in ev["j2"]), [])
+    assert ev["j2"][-1][1] == "abort" and got == chain(joined["j2"], len(got)) and len(got) < 40
+
+
+def test_logprobs_read_from_the_verify_rows(engine):
+    llm = engine()
+    o = llm.generate([[5, 6, 7]], SamplingParams(max_tokens=8, ignore_eos=True, logprobs=1))[0].outputs[0]
+    assert len(o.logprobs) == 8
+    want = -math.log1p((V - 1) * math.exp(-10.0))         # one-hot logit 10 over V tokens
+    for t, d in zip(o.token_ids, o.logprobs):
+        assert max(d, key=d.get) == t and abs(d[t] - want) < 1e-4   # the predicting row of each token
