@@ -179,3 +179,35 @@ def test_logprobs_read_from_the_verify_rows(engine):
     want = -math.log1p((V - 1) * math.exp(-10.0))         # one-hot logit 10 over V tokens
     for t, d in zip(o.token_ids, o.logprobs):
         assert max(d, key=d.get) == t and abs(d[t] - want) < 1e-4   # the predicting row of each token
+
+
+def test_gate_promotes_replays_and_logs(engine, tmp_path):
+    """The confidence gate in the decode loop: an always-firing gate promotes the step's
+    routed experts into a (CPU) delta tier, replays the step from its snapshot and logs
+    each evaluation; the replayed steps still give the model's chain."""
+    import json
+    from vllm_moet_b200.residency import ConfidenceGate
+    from vllm_moet_b200.residency.delta import DeltaTier, delta_layout
+    from vllm_moet_b200.utils.observability import DeltaTrace, JsonlWriter
+    llm = engine()
+    L, E, H, I = 2, 8, 64, 64
+    sb = delta_layout(H, I)[0]
+    llm.delta = DeltaTier([torch.zeros(E, sb, dtype=torch.uint8) for _ in range(L)], H, I, 16, device="cpu",
+                          policy="need")
+    llm.gate = ConfidenceGate(tau=2.0, fp_max=2)          # max-prob <= 1 < tau: always fires
+    llm.delta_trace = DeltaTrace(level=2, every=10 ** 6)
+    llm.gate_log = JsonlWriter(str(tmp_path / "gate.jsonl"))
+    llm.ecfg.moet.gate_fire_timing = False
+    # the fake model routes each row to experts derived from its pending token, in every layer
+    llm.runner.route_ids = lambda B, st=None: [torch.tensor([[int(t) % E, (int(t) + 1) % E] for t in
+                                                             llm._states[B].tokens[:, 0].tolist()])] * L
+    try:
+        out = llm.generate([[5, 6, 7]], SamplingParams(max_tokens=10, ignore_eos=True))[0].outputs[0].token_ids
+    finally:
+        llm.delta.close()
+        llm.gate_log.close()
+    assert out == chain([5, 6, 7], 10)
+    assert llm.delta.stats["gate_replays"] > 0 and llm.delta.stats["fetched_rows"] > 0
+    rows = [json.loads(x) for x in (tmp_path / "gate.jsonl").read_text().splitlines()]
+    assert len(rows) == llm._decode_steps and rows[0]["fired"] >= 1 and rows[0]["iters"][0]["promoted"] > 0
+    assert llm.delta_trace.snapshot(llm.delta)["resident"] > 0
