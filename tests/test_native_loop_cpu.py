@@ -211,3 +211,37 @@ def test_gate_promotes_replays_and_logs(engine, tmp_path):
     rows = [json.loads(x) for x in (tmp_path / "gate.jsonl").read_text().splitlines()]
     assert len(rows) == llm._decode_steps and rows[0]["fired"] >= 1 and rows[0]["iters"][0]["promoted"] > 0
     assert llm.delta_trace.snapshot(llm.delta)["resident"] > 0
+
+
+def test_base_cache_misses_are_fetched_and_replayed(engine):
+    """The expert-cache branch of the loop: the fake step counts routed experts whose slot
+    is -1 into the cache's miss counter (as the expert kernels do); the loop fetches them,
+    restores the step's state and replays until the step is miss-free."""
+    from vllm_moet_b200.residency import ExpertCache, ReplayEngine, make_store
+    from vllm_moet_b200.utils.observability import KpiLogger
+    llm = engine()
+    L, E, SB = 2, 8, 256
+    st_ = make_store("pinned", L, E, SB)
+    for li in range(L):
+        st_.add_layer(li, torch.randint(0, 256, (E, SB), dtype=torch.uint8))
+    cache = ExpertCache(st_, L, E, SB, 10, device="cpu", manager=False)   # one step needs <= 8 of 16
+    llm.cache, llm.replay, llm.kpi = cache, ReplayEngine(cache, comm_device="cpu"), KpiLogger(every=10 ** 6)
+    route = {}
+
+    def route_ids(B):
+        return route.get(B, [None] * L)
+    llm.runner.route_ids = route_ids
+    real_step = llm.runner.decode_body
+
+    def step_with_routing(st):
+        toks = st.tokens[:, 0].clone()
+        real_step(st)
+        ids = torch.tensor([[int(t) % E, (int(t) + 3) % E] for t in toks.tolist()])
+        route[st.B] = [ids] * L
+        for li in range(L):
+            cache.miss_count += int((cache.slot_table[li, ids.reshape(-1)] < 0).sum())
+    llm.runner.decode_body = step_with_routing
+    out = llm.generate([[5, 6, 7], [9, 9]], SamplingParams(max_tokens=9, ignore_eos=True))
+    assert [o.outputs[0].token_ids for o in out] == [chain([5, 6, 7], 9), chain([9, 9], 9)]
+    assert llm.replay.stats["replayed_steps"] > 0 and cache.stats["fetched_rows"] > 0
+    assert llm.kpi.snapshot()["replayed_steps"] == llm.replay.stats["replayed_steps"]
