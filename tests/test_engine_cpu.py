@@ -238,3 +238,25 @@ def test_prompt_logprobs_match_reference():
         d = o.prompt_logprobs[i]
         assert abs(d[p[i]] - float(lp[i - 1, p[i]])) < 1e-4 and len(d) <= 3
     assert llm.generate([p], SamplingParams(max_tokens=2))[0].prompt_logprobs is None
+
+
+def test_prefix_caching_reuses_the_shared_prefix():
+    """Automatic prefix caching: requests that share a block-aligned prompt prefix run the
+    main model on the suffix only (and the MTP prefill from the prefix's last position),
+    and give the same tokens, prompt logprobs and drafts-driven acceptance as a cold run."""
+    from vllm_moet_b200 import SamplingParams
+    sys_prompt = list(range(3, 3 + 40))
+    prompts = [sys_prompt + [50, 51, 52], sys_prompt + [60, 61], sys_prompt + [50, 51, 52, 53, 54, 55]]
+    sp = SamplingParams(max_tokens=10, ignore_eos=True, prompt_logprobs=1)
+    cold = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+    warm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256,
+               enable_prefix_caching=True, prefix_block_size=16)
+    want = [cold.generate([p], sp)[0] for p in prompts]
+    got = [warm.generate([p], sp)[0] for p in prompts]
+    for w, g in zip(want, got):
+        assert g.outputs[0].token_ids == w.outputs[0].token_ids
+        for a, b in zip(w.prompt_logprobs[1:], g.prompt_logprobs[1:]):
+            assert a.keys() == b.keys() and all(abs(a[t] - b[t]) < 1e-3 for t in a)
+    st = warm.runner.prefix_stats
+    assert st["hits"] == 2 and st["hit_tokens"] == 32 + 32      # block 16: 32 of the 40 shared tokens
+    assert cold.runner.prefix_stats["hits"] == 0

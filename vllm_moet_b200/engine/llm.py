@@ -54,7 +54,8 @@ class LLM:
                  delta_slots: int = 0, gate: Optional[bool] = None, expert_parallel: bool = False,
                  expert_store: str = "pinned", expert_store_dir: Optional[str] = None, sp_group=None,
                  dcp_group=None, dcp_interleave: int = 1, ep_group=None, speculative_method: str = "mtp",
-                 dspark: Optional[dict] = None, **model_overrides):
+                 dspark: Optional[dict] = None, enable_prefix_caching: bool = False,
+                 prefix_block_size: int = 16, **model_overrides):
         from ..models.loader import hf_config, is_checkpoint_dir, load_weights
         ckpt = model if is_checkpoint_dir(model) else None
         if ckpt is not None:
@@ -82,6 +83,10 @@ class LLM:
             raise ValueError(f"speculative_method {speculative_method!r}: mtp | dspark")
         if speculative_method == "dspark" and self.device.type == "cuda":
             raise NotImplementedError("DSpark block drafting runs on the CPU engine; the GPU runner drafts with MTP")
+        if enable_prefix_caching and self.device.type == "cuda":
+            raise NotImplementedError("prefix caching runs on the CPU engine; GPU prefill starts at position 0")
+        if enable_prefix_caching and (sp_group is not None or dcp_group is not None):
+            raise ValueError("prefix caching keeps whole per-sequence caches: not with SP prefill / DCP decode")
         if self.device.type == "cuda" and cfg.expert_scale != "ue8m0":
             cfg = cfg.replace(expert_scale="ue8m0")
         if self.device.type == "cuda" and cfg.dense_dtype != "fp8":
@@ -162,7 +167,8 @@ class LLM:
             self.runner = TorchRunner(self.mw, self.k, max_model_len, self.device, tp_group=tp_group,
                                       sp_group=sp_group, dcp_group=dcp_group, dcp_interleave=dcp_interleave,
                                       ep_group=ep_group,
-                                      dspark=(dspark or {}) if speculative_method == "dspark" else None)
+                                      dspark=(dspark or {}) if speculative_method == "dspark" else None,
+                                      prefix_block=prefix_block_size if enable_prefix_caching else 0)
 
     def _attach_tracing(self):
         """Prefill span timers, routing capture, delta trace / dump and the gate JSONL

@@ -14,7 +14,8 @@ from ..models.weights import ModelWeights
 
 class TorchRunner:
     def __init__(self, mw: ModelWeights, k: int, max_len: int, device="cpu", tp_group=None, sp_group=None,
-                 dcp_group=None, dcp_interleave: int = 1, ep_group=None, dspark: Optional[dict] = None):
+                 dcp_group=None, dcp_interleave: int = 1, ep_group=None, dspark: Optional[dict] = None,
+                 prefix_block: int = 0, prefix_entries: int = 64):
         self.mw = mw
         self.k = k if mw.mtp is not None and dspark is None else 0
         self.dspark = None              # DSpark block drafting instead of MTP: {drafter, tau, budget_frac}
@@ -29,6 +30,13 @@ class TorchRunner:
         self.rows = {}
         self.last_logits = {}           # row -> logits rows that predicted the tokens emitted by the last call
         self.prompt_logits = {}         # row -> logits of the prompt positions (prompt_logprobs)
+        # automatic prefix caching: block-aligned prompt prefix -> its main K/V, MTP K/V (one
+        # position shorter: the MTP entry of the prefix's last position needs the next token),
+        # last hidden state and logits
+        from collections import OrderedDict
+        self.prefix_block, self.prefix_entries = prefix_block, prefix_entries
+        self.prefix_cache: "OrderedDict" = OrderedDict()
+        self.prefix_stats = {"hits": 0, "hit_tokens": 0, "lookups": 0}
         self.tp_group = tp_group        # tensor-parallel CPU ranks (gloo): sharded weights, all-reduced partials
         self.sp_group = sp_group        # sequence-parallel prefill ranks: prompt chunks, gathered MLA latents
         self.dcp_group = dcp_group      # decode-context-parallel ranks: KV interleaved by position, LSE merge
@@ -78,11 +86,19 @@ class TorchRunner:
             n = len(prompt)
             main, mtp = self._kv(len(self.mw.layers)), self._kv(1)
             toks = torch.tensor(prompt, device=self.dev)
+            m, ent = 0, None
             if self.sp_group is not None:
                 from ..parallel.context import sp_prefill_forward
                 last, hid = sp_prefill_forward(self.mw, toks, self.cs, self.sp_group, main)
             else:
-                logits, hid = ref.forward(self.mw, toks, torch.arange(n, device=self.dev), self.cs, main)
+                m, ent = self._prefix_lookup(prompt)
+                if ent is not None:     # cached prefix: run the suffix only
+                    main, mtp = self._kv_copy(ent["main"]), self._kv_copy(ent["mtp"])
+                    ls, hs = ref.forward(self.mw, toks[m:], torch.arange(m, n, device=self.dev), self.cs, main)
+                    logits = torch.cat([ent["logits"], ls])
+                    hid = torch.cat([ent["hid"][None], hs])        # positions m-1 .. n-1 (MTP needs m-1)
+                else:
+                    logits, hid = ref.forward(self.mw, toks, torch.arange(n, device=self.dev), self.cs, main)
                 last = logits[-1]
                 self.prompt_logits[r] = logits[:-1]          # rows that predicted prompt tokens 1..n-1
             self.last_logits[r] = last[None]
@@ -93,18 +109,58 @@ class TorchRunner:
                 p = filter_probs(last[None], smp["sp"].temperature, smp["sp"].top_k, smp["sp"].top_p)
                 tgt = int(torch.multinomial(p[0], 1, generator=smp["gen"]))
             drafts = []
+            m0 = m - 1 if ent is not None else 0     # first MTP position to run
             if self.k:
-                nxt = torch.tensor(prompt[1:] + [tgt], device=self.dev)
-                ml, mh = ref.mtp_forward(self.mw, hid, nxt, torch.arange(n, device=self.dev), self.cs, mtp)
+                nxt = torch.tensor(prompt[1 + m0:] + [tgt], device=self.dev)
+                ml, mh = ref.mtp_forward(self.mw, hid, nxt, torch.arange(m0, n, device=self.dev), self.cs, mtp)
                 d = int(ml[-1].argmax()); drafts.append(d)
                 h = mh[-1:]
                 for j in range(1, self.k):
                     ml, h = ref.mtp_forward(self.mw, h, torch.tensor([d], device=self.dev),
                                             torch.tensor([n + j - 1], device=self.dev), self.cs, mtp)
                     d = int(ml[-1].argmax()); drafts.append(d)
+            if self.prefix_block and self.sp_group is None and self.dcp_group is None:
+                self._prefix_store(prompt, main, mtp, hid, logits, m0)
             self.rows[r] = dict(main=main, mtp=mtp, tokens=[tgt] + drafts, pos=n, sample=smp, hid=hid[-1])
             firsts.append(tgt)
         return firsts
+
+    # ------------------------------------------------------------------ prefix cache
+    @staticmethod
+    def _kv_copy(kv):
+        c = ref.RefKV(len(kv.k))
+        c.k, c.v = list(kv.k), list(kv.v)        # later appends concatenate into new tensors
+        return c
+
+    def _prefix_lookup(self, prompt):
+        """-> (m, entry) of the longest cached block-aligned prefix shorter than the prompt."""
+        if not self.prefix_block or self.sp_group is not None or self.dcp_group is not None:
+            return 0, None
+        self.prefix_stats["lookups"] += 1
+        b = self.prefix_block
+        for m in range((len(prompt) - 1) // b * b, 0, -b):
+            ent = self.prefix_cache.get(tuple(prompt[:m]))
+            if ent is not None:
+                self.prefix_cache.move_to_end(tuple(prompt[:m]))
+                self.prefix_stats["hits"] += 1
+                self.prefix_stats["hit_tokens"] += m
+                return m, ent
+        return 0, None
+
+    def _prefix_store(self, prompt, main, mtp, hid, logits, h0):
+        """Cache every block-aligned prefix of the prompt (hid rows start at position h0)."""
+        b = self.prefix_block
+        for m in range(b, len(prompt), b):
+            key = tuple(prompt[:m])
+            if key in self.prefix_cache or m - 1 < h0:     # (an evicted shorter prefix stays evicted)
+                self.prefix_cache.move_to_end(key)
+                continue
+            pm, pq = self._kv_copy(main), self._kv_copy(mtp)
+            pm.truncate(m)
+            pq.truncate(m - 1)
+            self.prefix_cache[key] = dict(main=pm, mtp=pq, hid=hid[m - 1 - h0], logits=logits[:m])
+            while len(self.prefix_cache) > self.prefix_entries:
+                self.prefix_cache.popitem(last=False)
 
     @torch.no_grad()
     def step(self, rows):

@@ -511,6 +511,9 @@ def build_parser():
     ap.add_argument("--pipeline-parallel-size", type=int, default=1)
     ap.add_argument("--decode-context-parallel-size", type=int, default=1)
     ap.add_argument("--enable-expert-parallel", action="store_true")
+    ap.add_argument("--enable-prefix-caching", action="store_true",
+                    help="reuse the K/V of shared block-aligned prompt prefixes (CPU engine)")
+    ap.add_argument("--block-size", type=int, default=16, help="prefix-cache block, in tokens")
     ap.add_argument("--gpus", default=None, help="GPU ids for the replicas of --data-parallel-size ('cpu': none)")
     ap.add_argument("--reasoning-parser", default="deepseek_v4", choices=_PARSERS)
     ap.add_argument("--tool-call-parser", default="deepseek_v4", choices=_PARSERS)
@@ -539,7 +542,9 @@ def llm_kwargs(args, world: int = 1, rank: int = 0, group=None) -> dict:
     return dict(device=args.device, num_speculative_tokens=k, max_model_len=args.max_model_len,
                 max_num_seqs=args.max_num_seqs, num_layers=args.num_layers, kv_cache_dtype=kv,
                 tensor_parallel_size=world, tp_group=group, tp_rank=rank,
-                expert_parallel=bool(args.enable_expert_parallel))
+                expert_parallel=bool(args.enable_expert_parallel),
+                enable_prefix_caching=bool(getattr(args, "enable_prefix_caching", False)),
+                prefix_block_size=int(getattr(args, "block_size", 16)))
 
 
 def main(argv=None):
