@@ -260,3 +260,23 @@ def test_prefix_caching_reuses_the_shared_prefix():
     st = warm.runner.prefix_stats
     assert st["hits"] == 2 and st["hit_tokens"] == 32 + 32      # block 16: 32 of the 40 shared tokens
     assert cold.runner.prefix_stats["hits"] == 0
+
+
+def test_hyper_connections_engine_matches_oracle():
+    """mHC model (4 residual streams, Sinkhorn-mixed around every block): the CPU engine's
+    MTP-speculative decode, with and without prefix caching, gives the full-recompute
+    greedy chain; the streams really mix (the model differs from the hc_mult 1 model)."""
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.models import reference as ref
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256, hc_mult=4,
+              enable_prefix_caching=True, prefix_block_size=4)
+    plain = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+    prompts = [[5, 6, 7, 8, 9, 10], [5, 6, 7, 8, 20]]
+    sp = SamplingParams(max_tokens=12, ignore_eos=True)
+    outs = [llm.generate([p], sp)[0].outputs[0].token_ids for p in prompts]
+    for p, o in zip(prompts, outs):
+        assert o == ref.greedy_generate(llm.mw, p, 12)
+    assert llm.runner.prefix_stats["hits"] == 1
+    assert outs[0] != plain.generate([prompts[0]], sp)[0].outputs[0].token_ids
+    with pytest.raises(NotImplementedError):
+        LLM("tiny-moe", device="cpu", hc_mult=4, speculative_method="dspark")

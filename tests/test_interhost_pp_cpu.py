@@ -13,13 +13,13 @@ from vllm_moet_b200.models.weights import random_weights
 from vllm_moet_b200.parallel.interhost_pp import Driver, Stage, recv_frame, send_frame, serve_stage
 
 
-def _cfg():
-    return tiny_config(num_layers=4)
+def _cfg(hc=1):
+    return tiny_config(num_layers=4, hc_mult=hc)
 
 
-def _chain(stages, rtt_ms=0.0):
+def _chain(stages, rtt_ms=0.0, hc=1):
     """Start stages 1..n-1 (listeners, last first) in threads; -> (driver, threads)."""
-    cfg = _cfg()
+    cfg = _cfg(hc)
     listeners = [socket.create_server(("127.0.0.1", 0)) for _ in range(stages - 1)]
     ports = [ls.getsockname()[1] for ls in listeners]
     threads = []
@@ -32,13 +32,14 @@ def _chain(stages, rtt_ms=0.0):
     return Driver(Stage(cfg, 0, stages), ("127.0.0.1", ports[0]), rtt_ms), threads, listeners
 
 
-@pytest.mark.parametrize("stages", [2, 3])
-def test_chain_matches_single_process(stages):
-    cfg = _cfg()
+@pytest.mark.parametrize("stages,hc", [(2, 1), (3, 1), (2, 4)])
+def test_chain_matches_single_process(stages, hc):
+    """(hc 4: hyper-connection streams [T, 4, H] cross the links.)"""
+    cfg = _cfg(hc)
     full = random_weights(cfg, "cpu", seed=0, with_mtp=False)
     prompt = [5, 9, 17, 33, 65, 129, 257, 513]
     want = reference.greedy_generate(full, prompt, 6)
-    d, threads, listeners = _chain(stages)
+    d, threads, listeners = _chain(stages, hc=hc)
     try:
         res = d.generate(prompt, 6)
         assert res["tokens"] == want

@@ -41,7 +41,7 @@ def _fp8_any(w):
     return q, s.float()
 
 
-def _make_ckpt(d, quant: bool, nvfp4_experts: bool = False, shards: int = 2):
+def _make_ckpt(d, quant: bool, nvfp4_experts: bool = False, shards: int = 2, hc: int = 1):
     g = torch.Generator().manual_seed(1)
     rn = lambda *s: torch.randn(*s, generator=g) * 0.05       # noqa: E731
     T = {"model.embed_tokens.weight": rn(V, H).to(torch.bfloat16), "model.norm.weight": 1 + rn(H) * 0.1,
@@ -89,6 +89,12 @@ def _make_ckpt(d, quant: bool, nvfp4_experts: bool = False, shards: int = 2):
                 expert(P + f"mlp.experts.{e}.gate_proj", rn(I, H))
                 expert(P + f"mlp.experts.{e}.up_proj", rn(I, H))
                 expert(P + f"mlp.experts.{e}.down_proj", rn(H, I))
+        if hc > 1:
+            for site in ("hc_attn", "hc_ffn"):
+                T[P + site + "_fn"], T[P + site + "_base"] = rn((2 + hc) * hc, hc * H), rn((2 + hc) * hc) * 10
+                T[P + site + "_scale"] = 1 + rn(3)
+            if li == L:
+                T[P + "hc_head_fn"], T[P + "hc_head_base"], T[P + "hc_head_scale"] = rn(hc, hc * H), rn(hc), 1 + rn(1)
         if li == L:
             T[P + "enorm.weight"] = 1 + rn(H) * 0.1
             T[P + "hnorm.weight"] = 1 + rn(H) * 0.1
@@ -104,8 +110,16 @@ def _make_ckpt(d, quant: bool, nvfp4_experts: bool = False, shards: int = 2):
         wm.update({n: fn for n in part})
     with open(os.path.join(d, "model.safetensors.index.json"), "w") as f:
         json.dump({"weight_map": wm}, f)
+    if hc > 1:
+        T["model.hc_head_fn"], T["model.hc_head_base"], T["model.hc_head_scale"] = rn(hc, hc * H), rn(hc), 1 + rn(1)
+        for n in ("model.hc_head_fn", "model.hc_head_base", "model.hc_head_scale"):
+            fn = "hc.safetensors"
+            wm[n] = fn
+        save_file({n: T[n] for n in wm if wm[n] == "hc.safetensors"}, os.path.join(d, "hc.safetensors"))
+        with open(os.path.join(d, "model.safetensors.index.json"), "w") as f:
+            json.dump({"weight_map": wm}, f)
     with open(os.path.join(d, "config.json"), "w") as f:
-        json.dump(_config(quant), f)
+        json.dump(dict(_config(quant), **({"hc_mult": hc, "hc_sinkhorn_iters": 10} if hc > 1 else {})), f)
     return T, raw
 
 
@@ -235,5 +249,24 @@ def test_loader_refuses_layouts_it_cannot_represent(tmp_path):
     idx = json.load(open(tmp_path / "model.safetensors.index.json"))
     idx["weight_map"]["model.layers.0.hc_pre_fn"] = "extra.safetensors"
     json.dump(idx, open(tmp_path / "model.safetensors.index.json", "w"))
-    with pytest.raises(NotImplementedError, match="hyper-connection"):
+    with pytest.raises(ValueError, match="hyper-connection"):      # hc tensors, config without hc_mult
         load_weights(str(tmp_path))
+
+
+def test_hyper_connection_checkpoint(tmp_path):
+    """mHC (hc_mult 2): the hc_* tensors land on every layer, the head and the MTP module,
+    and the engine serving the loaded model decodes the oracle's greedy chain."""
+    from vllm_moet_b200.engine.llm import LLM
+    from vllm_moet_b200.models import reference as ref
+    from vllm_moet_b200 import SamplingParams
+    T, _ = _make_ckpt(str(tmp_path), quant=False, shards=1, hc=2)
+    cfg = hf_config(str(tmp_path))
+    assert (cfg.hc_mult, cfg.hc_sinkhorn_iters) == (2, 10)
+    mw = load_weights(str(tmp_path))
+    assert torch.equal(mw.layers[1].hc_ffn.fn, T["model.layers.1.hc_ffn_fn"].float())
+    assert torch.equal(mw.extra["hc_head"].base, T["model.hc_head_base"].float())
+    assert torch.equal(mw.mtp.hc_head.scale, T[f"model.layers.{L}.hc_head_scale"].float())
+    llm = LLM(str(tmp_path), device="cpu", num_speculative_tokens=2, max_model_len=128)
+    prompt = [5, 17, 33, 2, 9]
+    out = llm.generate([prompt], SamplingParams(max_tokens=12, ignore_eos=True))[0].outputs[0].token_ids
+    assert out == ref.greedy_generate(llm.mw, prompt, 12)

@@ -9,9 +9,9 @@ from vllm_moet_b200.models import reference as ref
 from vllm_moet_b200.models.weights import random_weights
 
 
-def _tp_forward(rank, world):
+def _tp_forward(rank, world, hc=1):
     import torch.distributed as dist
-    cfg = tiny_config()
+    cfg = tiny_config(hc_mult=hc)
     toks = torch.tensor([5, 17, 300, 42, 7, 99, 3, 250])
     pos = torch.arange(len(toks))
     cs = ref.rope_cos_sin(cfg, 64)
@@ -27,8 +27,12 @@ def _tp_forward(rank, world):
             float((mtp_got - mtp_want).abs().max()), mw.lm_head.shape[0], cfg.vocab)
 
 
+def _tp_forward_hc(rank, world):
+    return _tp_forward(rank, world, hc=4)
+
+
 def test_tp2_forward_matches_single_rank():
-    res = run_ranks(_tp_forward, 2)
+    res = run_ranks(_tp_forward, 2) + run_ranks(_tp_forward_hc, 2)     # plain residual, then 4 hc streams
     for err, scale, mtp_err, v_local, vocab in res:
         assert v_local * 2 == vocab
         assert err <= 1e-4 * max(scale, 1.0), (err, scale)

@@ -51,6 +51,11 @@ class ModelConfig:
     index_topk: int = 2048
     # MTP
     num_mtp_layers: int = 1
+    # hyper-connections (mHC): hc_mult residual streams per token, mixed around every
+    # attention / FFN block; 1 = a plain residual
+    hc_mult: int = 1
+    hc_sinkhorn_iters: int = 20
+    hc_eps: float = 1e-6
     rope_theta: float = 10000.0
     rms_eps: float = 1e-6
     max_position: int = 163840
@@ -70,6 +75,8 @@ class ModelConfig:
             raise ValueError(f"unknown router {self.router!r}")
         if self.num_experts % self.n_group:
             raise ValueError("num_experts must divide into n_group groups")
+        if self.hc_mult < 1 or self.hc_sinkhorn_iters < 1:
+            raise ValueError("hc_mult and hc_sinkhorn_iters must be >= 1")
 
     @property
     def qk_head_dim(self) -> int:

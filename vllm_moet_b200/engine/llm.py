@@ -83,6 +83,12 @@ class LLM:
             raise ValueError(f"speculative_method {speculative_method!r}: mtp | dspark")
         if speculative_method == "dspark" and self.device.type == "cuda":
             raise NotImplementedError("DSpark block drafting runs on the CPU engine; the GPU runner drafts with MTP")
+        if cfg.hc_mult > 1 and self.device.type == "cuda":
+            raise NotImplementedError("hyper-connections (hc_mult > 1) run on the CPU engine; the GPU layer kernels "
+                                      "keep one residual stream")
+        if cfg.hc_mult > 1 and (sp_group is not None or speculative_method == "dspark"):
+            raise NotImplementedError("hyper-connections: not with SP prefill or DSpark drafting (both read a "
+                                      "single-stream hidden state)")
         if enable_prefix_caching and self.device.type == "cuda":
             raise NotImplementedError("prefix caching runs on the CPU engine; GPU prefill starts at position 0")
         if enable_prefix_caching and (sp_group is not None or dcp_group is not None):

@@ -17,7 +17,11 @@ slicing as the synthetic builder:
   conversion the reference's FP8 and NVFP4 paths end in -- then packed into
   fragment-major slots;
 * the MTP module (DeepSeek layout: decoder layer ``num_hidden_layers`` with
-  ``enorm``, ``hnorm``, ``eh_proj`` and ``shared_head.norm``).
+  ``enorm``, ``hnorm``, ``eh_proj`` -- or its ``e_proj`` / ``h_proj`` halves -- and
+  ``shared_head.norm``);
+* hyper-connections (``hc_mult`` > 1 in config.json): ``model.layers.{i}.hc_attn_*`` /
+  ``hc_ffn_*`` (``fn``, ``base``, ``scale``, f32), the head's ``model.hc_head_*`` and the
+  MTP layer's ``hc_head_*``.
 
 Names follow the DeepSeek-V3 layout (``model.layers.{i}.self_attn.q_a_proj`` ...,
 ``mlp.experts.{e}.gate_proj``, ``mlp.gate.e_score_correction_bias``).
@@ -33,7 +37,7 @@ import torch
 
 from ..config import ModelConfig
 from ..formats import codebook, planes
-from .weights import (ExpertLayout, ExpertPool, Fp8Linear, FloatLinear, LayerWeights, ModelWeights, MTPWeights,
+from .weights import (ExpertLayout, ExpertPool, Fp8Linear, FloatLinear, HyperConn, LayerWeights, ModelWeights, MTPWeights,
                       _derive_absorb, _shard_ffn, _vocab_shard, make_linear, pp_layer_range, tp_ffn_shard)
 
 
@@ -60,7 +64,9 @@ def hf_config(path: str, **overrides) -> ModelConfig:
         index_heads=c.get("index_n_heads", 0) or 0, index_head_dim=c.get("index_head_dim", 128) or 128,
         index_topk=c.get("index_topk", 2048) or 2048, num_mtp_layers=c.get("num_nextn_predict_layers", 0) or 0,
         rope_theta=float(c.get("rope_theta", 10000.0)), rms_eps=float(c.get("rms_norm_eps", 1e-6)),
-        max_position=c.get("max_position_embeddings", 163840), dense_dtype=dense)
+        max_position=c.get("max_position_embeddings", 163840), dense_dtype=dense,
+        hc_mult=int(c.get("hc_mult", 1) or 1), hc_sinkhorn_iters=int(c.get("hc_sinkhorn_iters", 20) or 20),
+        hc_eps=float(c.get("hc_eps", 1e-6)))
     if c.get("q_lora_rank") is None:
         raise NotImplementedError("checkpoints without q_lora_rank (no low-rank q) are not supported")
     kw.update(overrides)
@@ -248,11 +254,10 @@ def load_weights(path: str, cfg: Optional[ModelConfig] = None, device="cpu", tp_
         cfg = cfg.replace(expert_scale="ue8m0")
     dev = torch.device(device)
     rd = CheckpointReader(path)
-    unsupported = [n for n in rd.where if ".hc_" in n or n.startswith("hc_") or ".hc_head" in n]
-    if unsupported:
-        raise NotImplementedError(f"hyper-connection (mHC) tensors such as {unsupported[0]!r}: this engine's layers "
-                                  "have single residual streams, so the checkpoint would be served as a different "
-                                  "model")
+    has_hc = any(".hc_" in n or n.startswith("hc_") for n in rd.where)
+    if has_hc != (cfg.hc_mult > 1):
+        raise ValueError(f"config hc_mult={cfg.hc_mult} but the checkpoint "
+                         f"{'has' if has_hc else 'has no'} hyper-connection (hc_*) tensors")
     H = cfg.hidden
     L = cfg.num_layers if num_layers is None else num_layers
     l0, l1 = pp_layer_range(L, pp_rank, pp_size)
@@ -271,7 +276,8 @@ def load_weights(path: str, cfg: Optional[ModelConfig] = None, device="cpu", tp_
                       lm_head=head, tp_rank=tp_rank, tp_size=tp_size)
     mw.extra.update(layer_range=(l0, l1), pp_rank=pp_rank, pp_size=pp_size, checkpoint=path)
     N = cfg.num_layers
-    if with_mtp and cfg.num_mtp_layers and last and rd.has(f"model.layers.{N}.eh_proj.weight"):
+    split_eh = rd.has(f"model.layers.{N}.e_proj.weight") and rd.has(f"model.layers.{N}.h_proj.weight")
+    if with_mtp and cfg.num_mtp_layers and last and (rd.has(f"model.layers.{N}.eh_proj.weight") or split_eh):
         P = f"model.layers.{N}."
         if mw.embed is None:
             src = P + "embed_tokens.weight" if rd.has(P + "embed_tokens.weight") else "model.embed_tokens.weight"
@@ -279,9 +285,21 @@ def load_weights(path: str, cfg: Optional[ModelConfig] = None, device="cpu", tp_
         mw.mtp = MTPWeights(
             enorm=rd.get(P + "enorm.weight").to(torch.bfloat16).to(dev),
             hnorm=rd.get(P + "hnorm.weight").to(torch.bfloat16).to(dev),
-            eh_proj=rd.linear(P + "eh_proj", cfg.dense_dtype),
+            # DeepSeek-V4 stores the projection as separate embedding / hidden halves
+            eh_proj=(make_linear(torch.cat([rd.dense64(P + "e_proj"), rd.dense64(P + "h_proj")], 1).float(),
+                                 cfg.dense_dtype) if split_eh else rd.linear(P + "eh_proj", cfg.dense_dtype)),
             layer=_layer(rd, cfg, N, dev, True, tp_rank, tp_size, expert_parallel, expert_source),
             head_norm=rd.get(P + "shared_head.norm.weight").to(torch.bfloat16).to(dev))
+    if cfg.hc_mult > 1:
+        for i, lw in zip(range(l0, l1), mw.layers):
+            lw.hc_attn, lw.hc_ffn = _hc_site(rd, f"model.layers.{i}.hc_attn", dev), \
+                _hc_site(rd, f"model.layers.{i}.hc_ffn", dev)
+        if last:
+            mw.extra["hc_head"] = _hc_site(rd, "model.hc_head", dev)
+        if mw.mtp is not None:
+            P = f"model.layers.{N}."
+            mw.mtp.layer.hc_attn, mw.mtp.layer.hc_ffn = _hc_site(rd, P + "hc_attn", dev), _hc_site(rd, P + "hc_ffn", dev)
+            mw.mtp.hc_head = _hc_site(rd, P + "hc_head", dev)
     for lw in mw.layers + ([mw.mtp.layer] if mw.mtp is not None else []):
         for name in ("qkv_a", "q_b", "kv_b", "o", "gate_up", "down", "shared_gate_up", "shared_down", "w_uk_t",
                      "w_uv", "idx_wq", "idx_wk", "idx_ww"):
@@ -293,6 +311,11 @@ def load_weights(path: str, cfg: Optional[ModelConfig] = None, device="cpu", tp_
     if mw.mtp is not None:
         mw.mtp.eh_proj = mw.mtp.eh_proj.to(dev)
     return mw
+
+
+def _hc_site(rd: CheckpointReader, prefix: str, dev) -> HyperConn:
+    """`prefix`_fn / _base / _scale (f32, replicated on every TP rank)."""
+    return HyperConn(*(rd.get(f"{prefix}_{k}").float().to(dev) for k in ("fn", "base", "scale")))
 
 
 def is_checkpoint_dir(path) -> bool:

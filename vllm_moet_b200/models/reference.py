@@ -246,7 +246,58 @@ def attention(cfg: ModelConfig, lw: LayerWeights, x: torch.Tensor, positions: to
     return o.transpose(0, 1).reshape(T, Hh * vd) @ lw.o.dequant().t()
 
 
+# ------------------------------------------------------------------ hyper-connections (mHC)
+# The residual is n = hc_mult streams per token, x [T, n, H].  Around each block one
+# set of mixes is computed from the RMS-scaled flattened streams (DeepSeek-V4's mHC;
+# reference model: the upstream DeepSeek-V4 decoder layer, ``hc_pre`` / ``hc_post``):
+#   pre  = sigmoid(m[:n] s0 + b[:n]) + eps           block input = sum_i pre_i x_i
+#   post = 2 sigmoid(m[n:2n] s1 + b[n:2n])            weight of the block output per stream
+#   comb = softmax_j(m[2n:] s2 + b[2n:]) made doubly stochastic by Sinkhorn iterations
+#   x'_j = sum_i comb_ij x_i + post_j * block(...)
+def _hc_mixes(cfg, hc, x):
+    T, n, H = x.shape
+    flat = x.reshape(T, n * H).float()
+    return (flat @ hc.fn.float().t()) * torch.rsqrt(flat.square().mean(-1, keepdim=True) + cfg.rms_eps)
+
+
+def hc_pre(cfg, hc, x):
+    """x [T, n, H] -> (block input [T, H], post [T, n], comb [T, n, n])."""
+    T, n, _ = x.shape
+    m = _hc_mixes(cfg, hc, x)
+    b, s, eps = hc.base.float(), hc.scale.float(), cfg.hc_eps
+    pre = torch.sigmoid(m[:, :n] * s[0] + b[:n]) + eps
+    post = 2.0 * torch.sigmoid(m[:, n:2 * n] * s[1] + b[n:2 * n])
+    comb = torch.softmax(m[:, 2 * n:].view(T, n, n) * s[2] + b[2 * n:].view(n, n), dim=-1) + eps
+    comb = comb / (comb.sum(-2, keepdim=True) + eps)
+    for _ in range(cfg.hc_sinkhorn_iters - 1):
+        comb = comb / (comb.sum(-1, keepdim=True) + eps)
+        comb = comb / (comb.sum(-2, keepdim=True) + eps)
+    return (pre[..., None] * x.float()).sum(1), post, comb
+
+
+def hc_post(out, x, post, comb):
+    """Block output [T, H] back into the streams: x'_j = sum_i comb_ij x_i + post_j out."""
+    return torch.einsum("tij,tih->tjh", comb, x.float()) + post[..., None] * out.float()[:, None, :]
+
+
+def hc_head(cfg, hc, x):
+    """Collapse the streams before the final norm: sum_i gate_i x_i with
+    gate = sigmoid(m s + b) + eps over the RMS-scaled flattened streams."""
+    gate = torch.sigmoid(_hc_mixes(cfg, hc, x) * hc.scale.float()[0] + hc.base.float()) + cfg.hc_eps
+    return (gate[..., None] * x.float()).sum(1)
+
+
 def decoder_layer(cfg, lw, x, positions, cs, cache=None, li=0):
+    """x [T, H], or [T, n, H] residual streams when the layer has hyper-connections."""
+    if lw.hc_attn is not None:
+        h, post, comb = hc_pre(cfg, lw.hc_attn, x)
+        a = _allreduce((_ATTN_IMPL or attention)(cfg, lw, rms_norm(h, lw.attn_norm, cfg.rms_eps), positions, cs,
+                                                 cache, li))
+        x = hc_post(a, x, post, comb)
+        h, post, comb = hc_pre(cfg, lw.hc_ffn, x)
+        h = rms_norm(h, lw.ffn_norm, cfg.rms_eps)
+        f = _allreduce((_MOE_IMPL or moe_block)(cfg, lw, h) if lw.is_moe else dense_ffn(cfg, lw, h))
+        return hc_post(f, x, post, comb)
     h = rms_norm(x, lw.attn_norm, cfg.rms_eps)
     x = x + _allreduce((_ATTN_IMPL or attention)(cfg, lw, h, positions, cs, cache, li))
     h = rms_norm(x, lw.ffn_norm, cfg.rms_eps)
@@ -255,11 +306,17 @@ def decoder_layer(cfg, lw, x, positions, cs, cache=None, li=0):
 
 def forward(mw: ModelWeights, tokens: torch.Tensor, positions: torch.Tensor, cs: torch.Tensor,
             cache: Optional[RefKV] = None):
-    """-> (logits [T, V] f32, final normed hidden [T, H] f32)."""
+    """-> (logits [T, V] f32, the hidden state the MTP module reads: the final normed
+    hidden [T, H] f32, or with hyper-connections the streams before the head [T, n H])."""
     cfg = mw.cfg
     x = mw.embed[tokens].float()
+    if cfg.hc_mult > 1:
+        x = x[:, None, :].expand(-1, cfg.hc_mult, -1)
     for li, lw in enumerate(mw.layers):
         x = decoder_layer(cfg, lw, x, positions, cs, cache, li)
+    if cfg.hc_mult > 1:
+        h = rms_norm(hc_head(cfg, mw.extra["hc_head"], x), mw.final_norm, cfg.rms_eps)
+        return _gather_vocab(h @ mw.lm_head.dequant().t()), x.reshape(x.shape[0], -1)
     h = rms_norm(x, mw.final_norm, cfg.rms_eps)
     return _gather_vocab(h @ mw.lm_head.dequant().t()), h
 
@@ -268,12 +325,34 @@ def mtp_forward(mw: ModelWeights, hidden: torch.Tensor, next_tokens: torch.Tenso
                 cs: torch.Tensor, cache: Optional[RefKV] = None):
     """MTP module: (h_i, token_{i+1}) at position i -> logits for token_{i+2}; returns (logits, hidden)."""
     cfg, m = mw.cfg, mw.mtp
+    if cfg.hc_mult > 1:
+        return _mtp_forward_hc(mw, hidden, next_tokens, positions, cs, cache)
     e = rms_norm(mw.embed[next_tokens].float(), m.enorm, cfg.rms_eps)
     hn = rms_norm(hidden, m.hnorm, cfg.rms_eps)
     x = torch.cat([e, hn], dim=-1) @ m.eh_proj.dequant().t()
     x = decoder_layer(cfg, m.layer, x, positions, cs, cache, 0)
     h = rms_norm(x, m.head_norm, cfg.rms_eps)
     return _gather_vocab(h @ mw.lm_head.dequant().t()), h
+
+
+def _mtp_forward_hc(mw, hidden, next_tokens, positions, cs, cache):
+    """The MTP module over residual streams: `hidden` [T, n H] is the main model's (or
+    the previous draft's) pre-head streams.  Each stream is normed and projected by the
+    hidden half of eh_proj, the normed next-token embedding by its embedding half is
+    added to every stream (the embedding is zero at position 0, as DeepSeek-V4's MTP
+    masks it), then the MTP layer runs on the streams; logits come from the module's own
+    stream reduction, its head norm and the shared head.  -> (logits, streams [T, n H])."""
+    cfg, m = mw.cfg, mw.mtp
+    n, H = cfg.hc_mult, cfg.hidden
+    T = hidden.shape[0]
+    emb = mw.embed[next_tokens].float() * (positions != 0).float()[:, None]
+    e = rms_norm(emb, m.enorm, cfg.rms_eps)
+    hn = rms_norm(hidden.float().view(T, n, H), m.hnorm, cfg.rms_eps)
+    w = m.eh_proj.dequant().float()
+    x = hn @ w[:, H:].t() + (e @ w[:, :H].t())[:, None, :]
+    x = decoder_layer(cfg, m.layer, x, positions, cs, cache, 0)
+    h = rms_norm(hc_head(cfg, m.hc_head, x), m.head_norm, cfg.rms_eps)
+    return _gather_vocab(h @ mw.lm_head.dequant().t()), x.reshape(T, n * H)
 
 
 def greedy_generate(mw: ModelWeights, prompt: list, max_tokens: int) -> list:

@@ -197,10 +197,23 @@ class LayerWeights:
     idx_wq: object = None          # [Hi*D, q_lora] indexer queries (from the normed q_a)
     idx_wk: object = None          # [D, H] indexer key (from the normed hidden)
     idx_ww: object = None          # [Hi, H] per-head weights (softmax-free, scaled by 1/sqrt(Hi*D))
+    # hyper-connections (cfg.hc_mult > 1)
+    hc_attn: Optional["HyperConn"] = None
+    hc_ffn: Optional["HyperConn"] = None
 
     @property
     def is_moe(self) -> bool:
         return self.experts is not None
+
+
+@dataclass
+class HyperConn:
+    """Mixing parameters of one hyper-connection site (f32).  Around a block: `fn`
+    [(2 + n) n, n H] with `base` [(2 + n) n] and `scale` [3] give the pre / post /
+    n x n residual mixes; at a head: `fn` [n, n H], `base` [n], `scale` [1]."""
+    fn: torch.Tensor
+    base: torch.Tensor
+    scale: torch.Tensor
 
 
 @dataclass
@@ -210,6 +223,7 @@ class MTPWeights:
     eh_proj: object                # [H, 2H]
     layer: LayerWeights
     head_norm: torch.Tensor
+    hc_head: Optional[HyperConn] = None
 
 
 @dataclass
@@ -515,4 +529,34 @@ def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int =
             layer=_make_layer(cfg, rng, L, dev, True, tp_rank, tp_size, with_delta=with_delta, ep=expert_parallel,
                               expert_source=expert_source),
             head_norm=torch.ones(H, dtype=torch.bfloat16, device=dev))
+    if cfg.hc_mult > 1:
+        random_hyper_connections(mw, seed, L)
     return mw
+
+
+def random_hyper_connections(mw: ModelWeights, seed: int = 0, num_layers: Optional[int] = None) -> None:
+    """Random mHC parameters for every layer (and the MTP layer), plus the heads' reductions.
+    Drawn from their own generator, so the other weights match the hc_mult = 1 model."""
+    cfg = mw.cfg
+    n, H = cfg.hc_mult, cfg.hidden
+    dev = mw.final_norm.device
+    g = torch.Generator().manual_seed(seed * 7919 + 17)
+
+    def site(rows):
+        fn = torch.randn(rows, n * H, generator=g) * 0.02
+        base = torch.randn(rows, generator=g) * 0.5
+        scale = 0.5 + torch.rand(3 if rows > n else 1, generator=g)
+        return HyperConn(fn.to(dev), base.to(dev), scale.to(dev))
+    L = cfg.num_layers if num_layers is None else num_layers
+    l0 = mw.extra.get("layer_range", (0, len(mw.layers)))[0]
+    for i in range(L + 1):                         # one draw order whatever the PP slice
+        a, f = site((2 + n) * n), site((2 + n) * n)
+        if l0 <= i < l0 + len(mw.layers):
+            mw.layers[i - l0].hc_attn, mw.layers[i - l0].hc_ffn = a, f
+        elif i == L and mw.mtp is not None:
+            mw.mtp.layer.hc_attn, mw.mtp.layer.hc_ffn = a, f
+    head, mtp_head = site(n), site(n)
+    if mw.lm_head is not None:
+        mw.extra["hc_head"] = head
+    if mw.mtp is not None:
+        mw.mtp.hc_head = mtp_head

@@ -115,6 +115,8 @@ class Stage:
         """First stage: x = token ids [T]; others: x = hidden [T, H] (bf16 on the wire).
         -> hidden [T, H] bf16 (the tensor that crosses the link)."""
         h = self.mw.embed[x.to(self.dev).long()].float() if self.first else x.to(self.dev).float()
+        if self.first and self.cfg.hc_mult > 1:           # hyper-connections: [T, n, H] streams on the wire
+            h = h[:, None, :].expand(-1, self.cfg.hc_mult, -1)
         pos = positions.to(self.dev)
         for i, lw in enumerate(self.mw.layers):
             h = ref.decoder_layer(self.cfg, lw, h, pos, self.cs, self.cache, i)
@@ -122,7 +124,10 @@ class Stage:
 
     @torch.inference_mode()
     def head(self, h: torch.Tensor) -> int:
-        x = ref.rms_norm(h[-1:].float(), self.mw.final_norm, self.cfg.rms_eps)
+        h = h[-1:].float()
+        if self.cfg.hc_mult > 1:
+            h = ref.hc_head(self.cfg, self.mw.extra["hc_head"], h)
+        x = ref.rms_norm(h, self.mw.final_norm, self.cfg.rms_eps)
         return int((x @ self.mw.lm_head.dequant().t()).argmax(-1))
 
 
@@ -223,6 +228,7 @@ def main(argv=None):
     ap.add_argument("--stages", type=int, default=2)
     ap.add_argument("--model", default="tiny-moe")
     ap.add_argument("--num-layers", type=int, default=None)
+    ap.add_argument("--hc-mult", type=int, default=None, help="hyper-connection streams (model default)")
     ap.add_argument("--device", default="cpu")
     ap.add_argument("--port", type=int, default=29777, help="stage > 0: port to listen on")
     ap.add_argument("--next", default=None, help="stage > 0, not last: host:port of the next stage")
@@ -234,6 +240,8 @@ def main(argv=None):
     cfg = get_preset(args.model)
     if args.num_layers:
         cfg = cfg.replace(num_layers=args.num_layers)
+    if args.hc_mult:
+        cfg = cfg.replace(hc_mult=args.hc_mult)
     st = Stage(cfg, args.stage, args.stages, args.device)
     if args.stage > 0:
         ls = socket.create_server(("0.0.0.0", args.port))
