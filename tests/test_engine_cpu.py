@@ -280,3 +280,30 @@ def test_hyper_connections_engine_matches_oracle():
     assert outs[0] != plain.generate([prompts[0]], sp)[0].outputs[0].token_ids
     with pytest.raises(NotImplementedError):
         LLM("tiny-moe", device="cpu", hc_mult=4, speculative_method="dspark")
+
+
+def test_chunked_prefill_interleaves_with_decode():
+    """Chunked prefill: a long prompt is prefilled a token budget at a time while a short
+    request keeps decoding (its decode rows take (k + 1) tokens of each step's budget);
+    tokens and prompt logprobs equal the unchunked engine's, with and without prefix caching."""
+    from vllm_moet_b200 import SamplingParams
+    short, long_ = [5, 6, 7, 8], list(range(3, 63))
+    sp = SamplingParams(max_tokens=10, ignore_eos=True, prompt_logprobs=0)
+    plain = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+    want = plain.generate([short, long_], sp)
+    for prefix in (False, True):
+        llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256,
+                  enable_chunked_prefill=True, max_num_batched_tokens=8, enable_prefix_caching=prefix,
+                  prefix_block_size=16)
+        got = llm.generate([short, long_], sp)
+        for w, g in zip(want, got):
+            assert g.outputs[0].token_ids == w.outputs[0].token_ids
+            for a, b in zip(w.prompt_logprobs[1:], g.prompt_logprobs[1:]):
+                assert a.keys() == b.keys() and all(abs(a[t] - b[t]) < 1e-3 for t in a)
+        log = [c for c in llm._chunk_log if c[0] == got[1].request_id]
+        assert len(log) >= 10 and log[-1][2] == len(long_)
+        assert all(d - b <= 8 for _, b, d, _ in log)
+        assert sum(1 for c in log if c[3] == 1) >= 5             # chunks that ran beside a decoding row
+        assert llm.stats["prefill_chunks"] == len(llm._chunk_log)
+    with pytest.raises(NotImplementedError):
+        LLM("tiny-moe", device="cuda", enable_chunked_prefill=True)

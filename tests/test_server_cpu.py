@@ -187,6 +187,10 @@ def test_cli_flags_map_to_engine_arguments():
     kw = llm_kwargs(a)
     assert kw["num_speculative_tokens"] == 3 and kw["kv_cache_dtype"] == "nvfp4" and kw["expert_parallel"]
     assert a.reasoning_parser == "none" and a.served_model_name == "moet"
+    kw = llm_kwargs(build_parser().parse_args(["--enable-prefix-caching", "--block-size", "32",
+                                               "--enable-chunked-prefill", "--max-num-batched-tokens", "512"]))
+    assert kw["enable_prefix_caching"] and kw["prefix_block_size"] == 32
+    assert kw["enable_chunked_prefill"] and kw["max_num_batched_tokens"] == 512
     for bad in (["--speculative-config", '{"method": "eagle"}'], ["--pipeline-parallel-size", "2"],
                 ["--decode-context-parallel-size", "2"]):
         with pytest.raises(SystemExit):

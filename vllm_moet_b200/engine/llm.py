@@ -55,7 +55,8 @@ class LLM:
                  expert_store: str = "pinned", expert_store_dir: Optional[str] = None, sp_group=None,
                  dcp_group=None, dcp_interleave: int = 1, ep_group=None, speculative_method: str = "mtp",
                  dspark: Optional[dict] = None, enable_prefix_caching: bool = False,
-                 prefix_block_size: int = 16, **model_overrides):
+                 prefix_block_size: int = 16, enable_chunked_prefill: bool = False,
+                 max_num_batched_tokens: Optional[int] = None, **model_overrides):
         from ..models.loader import hf_config, is_checkpoint_dir, load_weights
         ckpt = model if is_checkpoint_dir(model) else None
         if ckpt is not None:
@@ -89,6 +90,16 @@ class LLM:
         if cfg.hc_mult > 1 and (sp_group is not None or speculative_method == "dspark"):
             raise NotImplementedError("hyper-connections: not with SP prefill or DSpark drafting (both read a "
                                       "single-stream hidden state)")
+        self._chunk_budget = None
+        if enable_chunked_prefill:
+            if self.device.type == "cuda":
+                raise NotImplementedError("chunked prefill runs on the CPU engine; the GPU prefill kernels start "
+                                          "at position 0")
+            if sp_group is not None or dcp_group is not None or ep_group is not None:
+                raise ValueError("chunked prefill: not with SP prefill, DCP decode or DP + EP")
+            self._chunk_budget = int(max_num_batched_tokens or 2048)
+            if self._chunk_budget < 1:
+                raise ValueError("max_num_batched_tokens must be >= 1")
         if enable_prefix_caching and self.device.type == "cuda":
             raise NotImplementedError("prefix caching runs on the CPU engine; GPU prefill starts at position 0")
         if enable_prefix_caching and (sp_group is not None or dcp_group is not None):
@@ -494,8 +505,13 @@ class LLM:
         B = self.ecfg.max_num_seqs if self._between is not None else max(1, min(len(reqs), self.ecfg.max_num_seqs))
         rows = [None] * B
         steps = accepted = 0
+        prefilling = {}                 # row -> request whose chunked prefill is in progress
+        self._decode_rows_last = 0
+        self._chunk_log = []
+
         def release(r):
             rows[r.row] = None
+            prefilling.pop(r.row, None)
             self.runner.release(r.row)
         ep = self._ep_group
 
@@ -517,6 +533,9 @@ class LLM:
             while waiting and free:
                 r = waiting.popleft(); r.row = free.pop(0); rows[r.row] = r; adm.append(r)
             n_pref = group_max(len(adm))
+            if self._chunk_budget is not None:
+                self._chunked_prefills(adm, rows, prefilling)
+                adm = []
             if adm:
                 firsts = self.runner.prefill([r.prompt for r in adm], [r.row for r in adm], [r.params for r in adm])
                 for r, f in zip(adm, firsts):
@@ -530,12 +549,13 @@ class LLM:
                         rows[r.row] = None; self.runner.release(r.row)
             if ep is not None:
                 self.runner.dummy_rows(n_pref - len(adm))
-            live = [i for i, r in enumerate(rows) if r is not None]
+            live = [i for i, r in enumerate(rows) if r is not None and r.row not in prefilling]
             n_step = group_max(len(live))
             if not live:
                 if ep is not None:
                     self.runner.dummy_rows(n_step)
                 continue
+            self._decode_rows_last = len(live)
             res = self.runner.step(live)
             if ep is not None:
                 self.runner.dummy_rows(n_step - len(live))
@@ -544,7 +564,39 @@ class LLM:
                 accepted += a
                 if self._emit(rows[i], toks, self.runner.last_logits.get(i)):
                     self.runner.release(i); rows[i] = None
-        self.stats = dict(steps=steps, accepted=accepted)
+        self.stats = dict(steps=steps, accepted=accepted, prefill_chunks=len(self._chunk_log))
+
+    def _chunked_prefills(self, adm, rows, prefilling):
+        """Chunked prefill: the step's token budget goes first to the running decode rows
+        ((k + 1) tokens each), the rest to prefills in arrival order, a chunk at a time, so a
+        long prompt never stalls the decoding rows for more than one budget of tokens.
+        A prefill that completes emits its first token; its row decodes from the next step."""
+        for r in adm:
+            self.runner.start_prefill(r.prompt, r.row, r.params)
+            prefilling[r.row] = r
+        n_dec = sum(1 for r in rows if r is not None and r.row not in prefilling)
+        budget = max(self._chunk_budget - n_dec * (self.k + 1), 1)       # prefills always advance
+        for row in list(prefilling):
+            if budget <= 0:
+                break
+            r = prefilling[row]
+            before = self.runner.partial[row]["done"]
+            f = self.runner.prefill_chunk(row, budget)
+            done = len(r.prompt) if f is not None else self.runner.partial[row]["done"]
+            budget -= done - before
+            self._chunk_log.append((r.rid, before, done, n_dec))
+            if f is None:
+                continue
+            del prefilling[row]
+            r.t_first = time.perf_counter()
+            pl = self.runner.prompt_logits.get(row)
+            if r.params.prompt_logprobs is not None and pl is not None:
+                from .sampling_params import logprob_entries
+                r.prompt_logprobs = [None] + (logprob_entries(pl, r.prompt[1:], r.params.prompt_logprobs)
+                                              if len(r.prompt) > 1 else [])
+            if self._emit(r, [f], self.runner.last_logits.get(row)):
+                rows[row] = None
+                self.runner.release(row)
 
     def _state(self, B):
         st = self._states.get(B)

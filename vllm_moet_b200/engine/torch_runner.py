@@ -30,6 +30,7 @@ class TorchRunner:
         self.rows = {}
         self.last_logits = {}           # row -> logits rows that predicted the tokens emitted by the last call
         self.prompt_logits = {}         # row -> logits of the prompt positions (prompt_logprobs)
+        self.partial = {}               # row -> state of a prefill in progress (chunked prefill)
         # automatic prefix caching: block-aligned prompt prefix -> its main K/V, MTP K/V (one
         # position shorter: the MTP entry of the prefix's last position needs the next token),
         # last hidden state and logits
@@ -82,48 +83,110 @@ class TorchRunner:
     def _prefill(self, prompts, rows, params):
         firsts = []
         for prompt, r, sp in zip(prompts, rows, params):
-            smp = self._sample_state(sp)
-            n = len(prompt)
-            main, mtp = self._kv(len(self.mw.layers)), self._kv(1)
-            toks = torch.tensor(prompt, device=self.dev)
-            m, ent = 0, None
             if self.sp_group is not None:
-                from ..parallel.context import sp_prefill_forward
-                last, hid = sp_prefill_forward(self.mw, toks, self.cs, self.sp_group, main)
-            else:
-                m, ent = self._prefix_lookup(prompt)
-                if ent is not None:     # cached prefix: run the suffix only
-                    main, mtp = self._kv_copy(ent["main"]), self._kv_copy(ent["mtp"])
-                    ls, hs = ref.forward(self.mw, toks[m:], torch.arange(m, n, device=self.dev), self.cs, main)
-                    logits = torch.cat([ent["logits"], ls])
-                    hid = torch.cat([ent["hid"][None], hs])        # positions m-1 .. n-1 (MTP needs m-1)
-                else:
-                    logits, hid = ref.forward(self.mw, toks, torch.arange(n, device=self.dev), self.cs, main)
-                last = logits[-1]
-                self.prompt_logits[r] = logits[:-1]          # rows that predicted prompt tokens 1..n-1
-            self.last_logits[r] = last[None]
-            if smp is None:
-                tgt = int(last.argmax())
-            else:
-                from ..spec.rejection import filter_probs
-                p = filter_probs(last[None], smp["sp"].temperature, smp["sp"].top_k, smp["sp"].top_p)
-                tgt = int(torch.multinomial(p[0], 1, generator=smp["gen"]))
-            drafts = []
-            m0 = m - 1 if ent is not None else 0     # first MTP position to run
-            if self.k:
-                nxt = torch.tensor(prompt[1 + m0:] + [tgt], device=self.dev)
-                ml, mh = ref.mtp_forward(self.mw, hid, nxt, torch.arange(m0, n, device=self.dev), self.cs, mtp)
-                d = int(ml[-1].argmax()); drafts.append(d)
-                h = mh[-1:]
-                for j in range(1, self.k):
-                    ml, h = ref.mtp_forward(self.mw, h, torch.tensor([d], device=self.dev),
-                                            torch.tensor([n + j - 1], device=self.dev), self.cs, mtp)
-                    d = int(ml[-1].argmax()); drafts.append(d)
-            if self.prefix_block and self.sp_group is None and self.dcp_group is None:
-                self._prefix_store(prompt, main, mtp, hid, logits, m0)
-            self.rows[r] = dict(main=main, mtp=mtp, tokens=[tgt] + drafts, pos=n, sample=smp, hid=hid[-1])
-            firsts.append(tgt)
+                firsts.append(self._prefill_sp(prompt, r, sp))
+                continue
+            self._start(prompt, r, sp)
+            firsts.append(self._chunk(r, len(prompt)))
         return firsts
+
+    # ------------------------------------------------------------------ chunked prefill
+    @torch.no_grad()
+    def start_prefill(self, prompt, r, sp=None):
+        """Begin a prefill that `prefill_chunk` advances a token budget at a time."""
+        self._start(prompt, r, sp)
+        return self.partial[r]["done"]
+
+    @torch.no_grad()
+    def prefill_chunk(self, r, budget: int):
+        """Run up to `budget` more prompt tokens of row r -> the first generated token when
+        the prompt is complete, else None."""
+        with self._ctx():
+            return self._chunk(r, budget)
+
+    def _start(self, prompt, r, sp):
+        m, ent = self._prefix_lookup(prompt)
+        if ent is not None:             # cached prefix: only the suffix runs
+            main, mtp = self._kv_copy(ent["main"]), self._kv_copy(ent["mtp"])
+            logits, hprev = [ent["logits"]], ent["hid"]
+        else:
+            main, mtp = self._kv(len(self.mw.layers)), self._kv(1)
+            logits, hprev = [], None
+        # invariant: main K/V covers [0, done), MTP K/V covers [0, done - 1) (the MTP entry of
+        # position p needs token p + 1); hprev is the hidden state at done - 1
+        self.partial[r] = dict(prompt=list(prompt), smp=self._sample_state(sp), main=main, mtp=mtp, done=m,
+                               hprev=hprev, logits=logits, bound={}, chunks=0)
+
+    def _chunk(self, r, budget):
+        st = self.partial[r]
+        prompt, main, mtp = st["prompt"], st["main"], st["mtp"]
+        n, s = len(prompt), st["done"]
+        e = min(n, s + max(1, budget))
+        ls, hs = ref.forward(self.mw, torch.tensor(prompt[s:e], device=self.dev),
+                             torch.arange(s, e, device=self.dev), self.cs, main)
+        st["logits"].append(ls)
+        st["chunks"] += 1
+        b = self.prefix_block
+        if b and self.dcp_group is None:
+            for m in range(-(-(s + 1) // b) * b, min(e, n - 1) + 1, b):      # prefixes ending in this chunk
+                st["bound"][m] = hs[m - 1 - s]
+        # MTP rows from position max(s - 1, 0): the hidden state of s - 1 came from the last chunk
+        hid = hs if s == 0 else torch.cat([st["hprev"][None], hs])
+        p0 = max(s - 1, 0)
+        st["done"], st["hprev"] = e, hs[-1]
+        if e < n:
+            if self.k and e - 1 > p0:
+                ref.mtp_forward(self.mw, hid[:-1], torch.tensor(prompt[p0 + 1:e], device=self.dev),
+                                torch.arange(p0, e - 1, device=self.dev), self.cs, mtp)
+            return None
+        logits = torch.cat(st["logits"])
+        last, smp = logits[-1], st["smp"]
+        self.prompt_logits[r] = logits[:-1]          # rows that predicted prompt tokens 1..n-1
+        self.last_logits[r] = last[None]
+        tgt = self._first_token(last, smp)
+        drafts = []
+        if self.k:
+            nxt = torch.tensor(prompt[p0 + 1:] + [tgt], device=self.dev)
+            ml, mh = ref.mtp_forward(self.mw, hid, nxt, torch.arange(p0, n, device=self.dev), self.cs, mtp)
+            drafts = self._chain_drafts(ml, mh, n, mtp)
+        for m, h in st["bound"].items():
+            self._prefix_put(prompt[:m], main, mtp, h, logits[:m])
+        self.rows[r] = dict(main=main, mtp=mtp, tokens=[tgt] + drafts, pos=n, sample=smp, hid=hid[-1])
+        del self.partial[r]
+        return tgt
+
+    def _first_token(self, last, smp):
+        if smp is None:
+            return int(last.argmax())
+        from ..spec.rejection import filter_probs
+        p = filter_probs(last[None], smp["sp"].temperature, smp["sp"].top_k, smp["sp"].top_p)
+        return int(torch.multinomial(p[0], 1, generator=smp["gen"]))
+
+    def _chain_drafts(self, ml, mh, n, mtp):
+        d = int(ml[-1].argmax())
+        drafts, h = [d], mh[-1:]
+        for j in range(1, self.k):
+            ml, h = ref.mtp_forward(self.mw, h, torch.tensor([d], device=self.dev),
+                                    torch.tensor([n + j - 1], device=self.dev), self.cs, mtp)
+            d = int(ml[-1].argmax()); drafts.append(d)
+        return drafts
+
+    def _prefill_sp(self, prompt, r, sp):
+        """Sequence-parallel prefill: the prompt's chunks on the SP ranks, gathered latents."""
+        from ..parallel.context import sp_prefill_forward
+        smp = self._sample_state(sp)
+        n = len(prompt)
+        main, mtp = self._kv(len(self.mw.layers)), self._kv(1)
+        last, hid = sp_prefill_forward(self.mw, torch.tensor(prompt, device=self.dev), self.cs, self.sp_group, main)
+        self.last_logits[r] = last[None]
+        tgt = self._first_token(last, smp)
+        drafts = []
+        if self.k:
+            nxt = torch.tensor(prompt[1:] + [tgt], device=self.dev)
+            ml, mh = ref.mtp_forward(self.mw, hid, nxt, torch.arange(n, device=self.dev), self.cs, mtp)
+            drafts = self._chain_drafts(ml, mh, n, mtp)
+        self.rows[r] = dict(main=main, mtp=mtp, tokens=[tgt] + drafts, pos=n, sample=smp, hid=hid[-1])
+        return tgt
 
     # ------------------------------------------------------------------ prefix cache
     @staticmethod
@@ -147,22 +210,19 @@ class TorchRunner:
                 return m, ent
         return 0, None
 
-    def _prefix_store(self, prompt, main, mtp, hid, logits, h0):
-        """Cache every block-aligned prefix of the prompt (hid rows start at position h0)."""
-        b = self.prefix_block
-        for m in range(b, len(prompt), b):
-            key = tuple(prompt[:m])
-            if key in self.prefix_cache or m - 1 < h0:     # (an evicted shorter prefix stays evicted)
-                self.prefix_cache.move_to_end(key)
-                continue
-            pm, pq = self._kv_copy(main), self._kv_copy(mtp)
-            pm.truncate(m)
-            pq.truncate(m - 1)
-            self.prefix_cache[key] = dict(main=pm, mtp=pq, hid=hid[m - 1 - h0], logits=logits[:m])
-            while len(self.prefix_cache) > self.prefix_entries:
-                self.prefix_cache.popitem(last=False)
+    def _prefix_put(self, key, main, mtp, hid, logits):
+        """Cache one block-aligned prefix (`hid`: the hidden state at its last position)."""
+        key, m = tuple(key), len(key)
+        if key in self.prefix_cache:
+            self.prefix_cache.move_to_end(key)
+            return
+        pm, pq = self._kv_copy(main), self._kv_copy(mtp)
+        pm.truncate(m)
+        pq.truncate(m - 1)
+        self.prefix_cache[key] = dict(main=pm, mtp=pq, hid=hid, logits=logits)
+        while len(self.prefix_cache) > self.prefix_entries:
+            self.prefix_cache.popitem(last=False)
 
-    @torch.no_grad()
     def step(self, rows):
         """-> {row: (emitted tokens list, n_accepted)}"""
         with self._ctx():
@@ -251,5 +311,6 @@ class TorchRunner:
 
     def release(self, r):
         self.rows.pop(r, None)
+        self.partial.pop(r, None)
         self.last_logits.pop(r, None)
         self.prompt_logits.pop(r, None)

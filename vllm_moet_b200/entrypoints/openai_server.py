@@ -514,6 +514,9 @@ def build_parser():
     ap.add_argument("--enable-prefix-caching", action="store_true",
                     help="reuse the K/V of shared block-aligned prompt prefixes (CPU engine)")
     ap.add_argument("--block-size", type=int, default=16, help="prefix-cache block, in tokens")
+    ap.add_argument("--enable-chunked-prefill", action="store_true",
+                    help="prefill long prompts a token budget per step beside the decoding rows (CPU engine)")
+    ap.add_argument("--max-num-batched-tokens", type=int, default=None, help="per-step token budget (chunked prefill)")
     ap.add_argument("--gpus", default=None, help="GPU ids for the replicas of --data-parallel-size ('cpu': none)")
     ap.add_argument("--reasoning-parser", default="deepseek_v4", choices=_PARSERS)
     ap.add_argument("--tool-call-parser", default="deepseek_v4", choices=_PARSERS)
@@ -544,7 +547,9 @@ def llm_kwargs(args, world: int = 1, rank: int = 0, group=None) -> dict:
                 tensor_parallel_size=world, tp_group=group, tp_rank=rank,
                 expert_parallel=bool(args.enable_expert_parallel),
                 enable_prefix_caching=bool(getattr(args, "enable_prefix_caching", False)),
-                prefix_block_size=int(getattr(args, "block_size", 16)))
+                prefix_block_size=int(getattr(args, "block_size", 16)),
+                enable_chunked_prefill=bool(getattr(args, "enable_chunked_prefill", False)),
+                max_num_batched_tokens=getattr(args, "max_num_batched_tokens", None))
 
 
 def main(argv=None):
