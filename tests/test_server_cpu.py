@@ -191,6 +191,11 @@ def test_cli_flags_map_to_engine_arguments():
                                                "--enable-chunked-prefill", "--max-num-batched-tokens", "512"]))
     assert kw["enable_prefix_caching"] and kw["prefix_block_size"] == 32
     assert kw["enable_chunked_prefill"] and kw["max_num_batched_tokens"] == 512
+    from vllm_moet_b200.entrypoints.openai_server import _params_from
+    sp = _params_from({"presence_penalty": 0.5, "frequency_penalty": 0.25, "repetition_penalty": 1.1,
+                       "min_p": 0.05, "logit_bias": {"42": -100}})
+    assert (sp.presence_penalty, sp.frequency_penalty, sp.repetition_penalty, sp.min_p) == (0.5, 0.25, 1.1, 0.05)
+    assert sp.logit_bias == {42: -100.0} and sp.processes_logits
     for bad in (["--speculative-config", '{"method": "eagle"}'], ["--pipeline-parallel-size", "2"],
                 ["--decode-context-parallel-size", "2"]):
         with pytest.raises(SystemExit):

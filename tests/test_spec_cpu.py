@@ -4,6 +4,8 @@ import math
 
 import torch
 
+from vllm_moet_b200 import SamplingParams
+from vllm_moet_b200.engine.llm import LLM
 from vllm_moet_b200.spec import DSparkDrafter, allocate_widths, greedy_accept, rejection_sample
 
 
@@ -169,3 +171,65 @@ def test_dspark_engine_verifies_blocks():
     out = llm.generate([p], SamplingParams(max_tokens=n, ignore_eos=True))[0].outputs[0].token_ids
     assert out == want
     assert llm.stats["accepted"] >= n - 4 and llm.stats["steps"] <= n // 5 + 2
+
+
+def _process_oracle(logits, sp, prompt, hist):
+    """One row, written out token by token (vLLM semantics)."""
+    x = logits.float().clone()
+    cnt = {}
+    for t in hist:
+        cnt[t] = cnt.get(t, 0) + 1
+    for t in set(hist) | set(prompt):
+        if sp.repetition_penalty != 1.0:
+            x[t] = x[t] / sp.repetition_penalty if x[t] > 0 else x[t] * sp.repetition_penalty
+    for t, c in cnt.items():
+        x[t] -= sp.frequency_penalty * c + sp.presence_penalty
+    for t, b in (sp.logit_bias or {}).items():
+        x[t] += b
+    return x
+
+
+def test_penalties_and_bias_per_verify_row():
+    """Row j of a verify pass is processed with the drafts before it counted as output."""
+    from vllm_moet_b200.spec.logits_process import process_logits
+    g = torch.Generator().manual_seed(0)
+    V = 64
+    logits = torch.randn(3, V, generator=g) * 3
+    sp = SamplingParams(repetition_penalty=1.3, frequency_penalty=0.4, presence_penalty=0.2,
+                        logit_bias={5: 2.0, 60: -1.5})
+    prompt, out, drafts = [1, 2, 3, 2], [7, 9, 7], [9, 11]
+    got = process_logits(logits, sp, prompt, out, drafts)
+    for j in range(3):
+        want = _process_oracle(logits[j], sp, prompt, out + drafts[:j])
+        assert torch.allclose(got[j], want, atol=1e-6), j
+    assert torch.equal(process_logits(logits, SamplingParams(), prompt, out, drafts), logits)
+
+
+def test_min_p_filter():
+    from vllm_moet_b200.spec.rejection import filter_probs
+    logits = torch.log(torch.tensor([[0.5, 0.3, 0.15, 0.05]]))
+    p = filter_probs(logits, 1.0, min_p=0.25)          # keeps p >= 0.125
+    assert torch.allclose(p, torch.tensor([[0.5, 0.3, 0.15, 0.0]]) / 0.95)
+
+
+def test_engine_penalties_match_token_by_token_decode():
+    """The speculative CPU engine with penalties and bias emits what plain one-token greedy
+    decoding over processed logits emits (drafts verified against processed rows)."""
+    from vllm_moet_b200.models import reference as ref
+    from vllm_moet_b200.spec.logits_process import process_logits
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+    sp = SamplingParams(max_tokens=16, ignore_eos=True, repetition_penalty=1.5, frequency_penalty=0.5,
+                        presence_penalty=0.3, logit_bias={100: 1.0})
+    prompt = [5, 6, 7, 5, 6]
+    got = llm.generate([prompt], sp)[0].outputs[0].token_ids
+    cs = ref.rope_cos_sin(llm.cfg, 64)
+    toks, out = list(prompt), []
+    for _ in range(16):
+        lg, _ = ref.forward(llm.mw, torch.tensor(toks), torch.arange(len(toks)), cs)
+        t = int(process_logits(lg[-1:], sp, prompt, out)[0].argmax())
+        out.append(t)
+        toks.append(t)
+    assert got == out
+    assert got != llm.generate([prompt], SamplingParams(max_tokens=16, ignore_eos=True))[0].outputs[0].token_ids
+    forced = llm.generate([prompt], SamplingParams(max_tokens=6, ignore_eos=True, logit_bias={42: 1e4}))
+    assert forced[0].outputs[0].token_ids == [42] * 6

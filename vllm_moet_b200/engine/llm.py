@@ -388,6 +388,12 @@ class LLM:
         if sp.temperature != 0 and self.device.type == "cuda":
             raise NotImplementedError("temperature > 0: the GPU runner verifies drafts greedily inside the "
                                       "decode graph; sampling is served by the CPU engine")
+        if sp.processes_logits or sp.min_p > 0:
+            if self.device.type == "cuda":
+                raise NotImplementedError("penalties / logit_bias / min_p: the GPU decode graph chooses tokens "
+                                          "from the raw logits; they are served by the CPU engine")
+            if getattr(self.runner, "sp_group", None) is not None or getattr(self.runner, "dspark", None):
+                raise NotImplementedError("penalties / logit_bias / min_p: not with SP prefill or DSpark drafting")
         if len(t) + sp.max_tokens + self.k + 1 > self.ecfg.max_model_len:
             raise ValueError(f"prompt ({len(t)}) + max_tokens ({sp.max_tokens}) exceeds max_model_len")
 

@@ -20,6 +20,12 @@ class SamplingParams:
     logprobs: Optional[int] = None  # per generated token: the chosen token's and the top-N log-probabilities
     n: int = 1                      # completions per prompt (copies i > 0 sample with seed + i when seeded)
     prompt_logprobs: Optional[int] = None   # per prompt token after the first: its and the top-N log-probabilities
+    # logits processing (CPU engine), in vLLM's semantics
+    presence_penalty: float = 0.0   # minus this for every token already generated
+    frequency_penalty: float = 0.0  # minus this times the token's count in the generated text
+    repetition_penalty: float = 1.0  # tokens of the prompt or the output: positive logits / r, negative * r
+    logit_bias: Optional[Dict[int, float]] = None   # token id -> added to its logit
+    min_p: float = 0.0              # sampling: drop tokens below min_p x the top token's probability
 
     def __post_init__(self):
         if isinstance(self.stop, str):
@@ -35,6 +41,20 @@ class SamplingParams:
             raise ValueError("temperature must be >= 0")
         if not 0 < self.top_p <= 1:
             raise ValueError("top_p must be in (0, 1]")
+        if self.repetition_penalty <= 0:
+            raise ValueError("repetition_penalty must be > 0")
+        if not 0 <= self.min_p <= 1:
+            raise ValueError("min_p must be in [0, 1]")
+        if not -2 <= self.presence_penalty <= 2 or not -2 <= self.frequency_penalty <= 2:
+            raise ValueError("presence_penalty and frequency_penalty must be in [-2, 2]")
+        if self.logit_bias:
+            self.logit_bias = {int(k): float(v) for k, v in self.logit_bias.items()}
+
+    @property
+    def processes_logits(self) -> bool:
+        """Whether the logits are changed before choosing a token (penalties, bias)."""
+        return bool(self.presence_penalty or self.frequency_penalty or self.repetition_penalty != 1.0
+                    or self.logit_bias)
 
 
 def find_stop(text: str, stops: List[str], start: int = 0):

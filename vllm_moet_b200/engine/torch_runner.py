@@ -10,6 +10,7 @@ import torch
 
 from ..models import reference as ref
 from ..models.weights import ModelWeights
+from ..spec.logits_process import process_logits
 
 
 class TorchRunner:
@@ -114,7 +115,7 @@ class TorchRunner:
             logits, hprev = [], None
         # invariant: main K/V covers [0, done), MTP K/V covers [0, done - 1) (the MTP entry of
         # position p needs token p + 1); hprev is the hidden state at done - 1
-        self.partial[r] = dict(prompt=list(prompt), smp=self._sample_state(sp), main=main, mtp=mtp, done=m,
+        self.partial[r] = dict(prompt=list(prompt), sp=sp, smp=self._sample_state(sp), main=main, mtp=mtp, done=m,
                                hprev=hprev, logits=logits, bound={}, chunks=0)
 
     def _chunk(self, r, budget):
@@ -143,7 +144,7 @@ class TorchRunner:
         last, smp = logits[-1], st["smp"]
         self.prompt_logits[r] = logits[:-1]          # rows that predicted prompt tokens 1..n-1
         self.last_logits[r] = last[None]
-        tgt = self._first_token(last, smp)
+        tgt = self._first_token(process_logits(last[None], st["sp"], prompt, [])[0], smp, st["sp"])
         drafts = []
         if self.k:
             nxt = torch.tensor(prompt[p0 + 1:] + [tgt], device=self.dev)
@@ -151,15 +152,16 @@ class TorchRunner:
             drafts = self._chain_drafts(ml, mh, n, mtp)
         for m, h in st["bound"].items():
             self._prefix_put(prompt[:m], main, mtp, h, logits[:m])
-        self.rows[r] = dict(main=main, mtp=mtp, tokens=[tgt] + drafts, pos=n, sample=smp, hid=hid[-1])
+        self.rows[r] = dict(main=main, mtp=mtp, tokens=[tgt] + drafts, pos=n, sample=smp, hid=hid[-1],
+                            sp=st["sp"], prompt=prompt, out=[tgt])
         del self.partial[r]
         return tgt
 
-    def _first_token(self, last, smp):
+    def _first_token(self, last, smp, sp=None):
         if smp is None:
             return int(last.argmax())
         from ..spec.rejection import filter_probs
-        p = filter_probs(last[None], smp["sp"].temperature, smp["sp"].top_k, smp["sp"].top_p)
+        p = filter_probs(last[None], smp["sp"].temperature, smp["sp"].top_k, smp["sp"].top_p, smp["sp"].min_p)
         return int(torch.multinomial(p[0], 1, generator=smp["gen"]))
 
     def _chain_drafts(self, ml, mh, n, mtp):
@@ -269,16 +271,18 @@ class TorchRunner:
             toks = torch.tensor(st["tokens"], device=self.dev)
             pos = torch.arange(p, p + k + 1, device=self.dev)
             logits, hid = ref.forward(self.mw, toks, pos, self.cs, st["main"])
-            smp = st.get("sample")
+            smp, sp = st.get("sample"), st.get("sp")
+            scores = logits if sp is None or not sp.processes_logits else \
+                process_logits(logits, sp, st["prompt"], st["out"], st["tokens"][1:])
             if smp is None:
-                tg = logits.argmax(-1).tolist()
+                tg = scores.argmax(-1).tolist()
                 a = 0
                 while a < k and st["tokens"][a + 1] == tg[a]:
                     a += 1
             else:       # speculative sampling: the MTP drafts are greedy, so q is one-hot
                 from ..spec.rejection import filter_probs, rejection_sample
                 sp = smp["sp"]
-                probs = filter_probs(logits, sp.temperature, sp.top_k, sp.top_p)      # [k+1, V]
+                probs = filter_probs(scores, sp.temperature, sp.top_k, sp.top_p, sp.min_p)     # [k+1, V]
                 d = toks[1:].long()
                 q = torch.nn.functional.one_hot(d, probs.shape[-1]).float()
                 n_acc, em = rejection_sample(probs[None], q[None], d[None], generator=smp["gen"])
@@ -299,6 +303,8 @@ class TorchRunner:
                     d = int(ml[-1].argmax()); drafts.append(d)
             st["tokens"] = [tg[a]] + drafts
             st["pos"] = p + a + 1
+            if "out" in st:
+                st["out"] += emitted
             out[r] = (emitted, a)
         return out
 

@@ -162,7 +162,12 @@ def _params_from(body: Dict[str, Any], default_max: int = 16) -> SamplingParams:
                           stop_token_ids=stop_ids, ignore_eos=bool(body.get("ignore_eos", False)),
                           stop=[stop] if isinstance(stop, str) else list(stop),
                           include_stop_str_in_output=bool(body.get("include_stop_str_in_output", False)),
-                          min_tokens=int(body.get("min_tokens") or 0), logprobs=lp, n=int(body.get("n") or 1))
+                          min_tokens=int(body.get("min_tokens") or 0), logprobs=lp, n=int(body.get("n") or 1),
+                          presence_penalty=float(body.get("presence_penalty") or 0.0),
+                          frequency_penalty=float(body.get("frequency_penalty") or 0.0),
+                          repetition_penalty=float(body.get("repetition_penalty") or 1.0),
+                          min_p=float(body.get("min_p") or 0.0),
+                          logit_bias={int(k): float(v) for k, v in (body.get("logit_bias") or {}).items()} or None)
 
 
 class _ChatParseStream:

@@ -1,0 +1,44 @@
+"""Logits processing before a token is chosen: repetition / presence / frequency
+penalties and logit bias, with vLLM's semantics (``SamplingParams`` fields of the same
+names).
+
+Speculative verify: row j of a verify pass scores the token after the pending token and
+drafts ``d_1 .. d_j``.  The drafts before it count as generated text for row j: if row j's
+choice is ever emitted, those drafts were all accepted, so the penalties see exactly the
+history that the token would have had in plain one-token decoding.
+"""
+from __future__ import annotations
+
+from typing import Optional, Sequence
+
+import torch
+
+
+def process_logits(logits: torch.Tensor, sp, prompt: Sequence[int], out: Sequence[int],
+                   drafts: Optional[Sequence[int]] = None) -> torch.Tensor:
+    """logits [R, V] (row j after `out` + drafts[:j]) -> processed logits [R, V] (f32)."""
+    x = logits.float().clone()
+    if sp is None or not sp.processes_logits:
+        return x
+    R, V = x.shape
+    drafts = list(drafts or [])[: max(R - 1, 0)]
+    dev = x.device
+    counts = torch.bincount(torch.as_tensor(list(out), dtype=torch.long, device=dev), minlength=V)[:V]
+    counts = counts[None].repeat(R, 1).float()
+    for j, d in enumerate(drafts):                 # row j + 1 and later saw draft j
+        counts[j + 1:, int(d)] += 1
+    if sp.repetition_penalty != 1.0:
+        seen = counts > 0
+        if len(prompt):
+            seen[:, torch.as_tensor(list(prompt), dtype=torch.long, device=dev)] = True
+        r = sp.repetition_penalty
+        x = torch.where(seen, torch.where(x > 0, x / r, x * r), x)
+    if sp.frequency_penalty:
+        x = x - sp.frequency_penalty * counts
+    if sp.presence_penalty:
+        x = x - sp.presence_penalty * (counts > 0).float()
+    if sp.logit_bias:
+        ids = torch.tensor([t for t in sp.logit_bias if 0 <= t < V], dtype=torch.long, device=dev)
+        if len(ids):
+            x[:, ids] += torch.tensor([sp.logit_bias[int(t)] for t in ids], device=dev)
+    return x

@@ -63,10 +63,15 @@ def rejection_sample(target_probs: torch.Tensor, draft_probs: torch.Tensor, draf
     return n_acc, emitted
 
 
-def filter_probs(logits: torch.Tensor, temperature: float, top_k: int = 0, top_p: float = 1.0) -> torch.Tensor:
-    """logits [R, V] -> probabilities [R, V]: softmax(logits / T) restricted to the top_k
-    tokens (0 = all) and to the smallest set whose probability reaches top_p (at least one)."""
+def filter_probs(logits: torch.Tensor, temperature: float, top_k: int = 0, top_p: float = 1.0,
+                 min_p: float = 0.0) -> torch.Tensor:
+    """logits [R, V] -> probabilities [R, V]: softmax(logits / T) without the tokens below
+    min_p x the top probability, restricted to the top_k tokens (0 = all) and to the
+    smallest set whose probability reaches top_p (at least one)."""
     x = logits.float() / max(temperature, 1e-6)
+    if min_p > 0:
+        p0 = torch.softmax(x, dim=-1)
+        x = x.masked_fill(p0 < min_p * p0.amax(-1, keepdim=True), float("-inf"))
     if top_k and 0 < top_k < x.shape[-1]:
         kth = torch.topk(x, top_k, dim=-1).values[..., -1:]
         x = x.masked_fill(x < kth, float("-inf"))
