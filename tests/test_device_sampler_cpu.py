@@ -1,0 +1,69 @@
+"""The graph-safe batch sampler (spec/device_sampler.py) on CPU tensors: greedy rows
+reproduce greedy verification, the emitted tokens follow token-by-token sampling from the
+filtered target distribution, filters hold, and draws are reproducible per seed and
+position."""
+import torch
+
+from vllm_moet_b200.spec.device_sampler import sample_verify, target_probs, uniform
+from vllm_moet_b200.spec.rejection import filter_probs, greedy_accept
+
+
+def _params(B, t=0.0, k=0, p=1.0, mp=0.0):
+    return (torch.full((B,), t), torch.full((B,), k, dtype=torch.int32), torch.full((B,), p), torch.full((B,), mp))
+
+
+def test_greedy_rows_equal_greedy_verification():
+    g = torch.Generator().manual_seed(0)
+    B, k, V = 16, 3, 50
+    logits = torch.randn(B, k + 1, V, generator=g)
+    am = logits.argmax(-1)
+    drafts = torch.where(torch.rand(B, k, generator=g) < 0.6, am[:, :k], torch.randint(0, V, (B, k), generator=g))
+    n, tok = sample_verify(logits, drafts, *_params(B), torch.arange(B), torch.full((B,), 7))
+    n_ref, em = greedy_accept(am, drafts)
+    assert torch.equal(n.long(), n_ref)
+    for b in range(B):
+        a = int(n_ref[b])
+        assert tok[b, : a + 1].tolist() == em[b, : a + 1].tolist() and (tok[b, a:] == tok[b, a]).all()
+
+
+def test_filters_match_filter_probs():
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(6, 40, generator=g) * 2
+    for t, k, p, mp in ((0.7, 0, 1.0, 0.0), (1.0, 5, 1.0, 0.0), (1.3, 0, 0.8, 0.0), (0.9, 10, 0.9, 0.05)):
+        got = target_probs(x, *_params(6, t, k, p, mp))
+        want = filter_probs(x, t, k, p, mp)
+        assert torch.allclose(got, want, atol=1e-6), (t, k, p, mp)
+
+
+def test_emitted_tokens_follow_sequential_sampling():
+    """First token ~ p_0; given the first token equals draft d_0, the second ~ p_1 (the
+    property that makes speculative sampling exact)."""
+    g = torch.Generator().manual_seed(2)
+    V, N = 6, 60000
+    base = torch.randn(3, V, generator=g)
+    logits = base[None].expand(N, -1, -1)
+    drafts = torch.tensor([[int(base[0].argmax()), int(base[1].argmax())]]).expand(N, -1)
+    t = 0.8
+    n, tok = sample_verify(logits, drafts, *_params(N, t, 0, 0.9), torch.arange(N), torch.full((N,), 11))
+    p = filter_probs(base, t, 0, 0.9)
+    f0 = torch.bincount(tok[:, 0].long(), minlength=V).float() / N
+    assert (f0 - p[0]).abs().max() < 0.01, (f0, p[0])
+    sel = tok[:, 0] == drafts[0, 0]
+    f1 = torch.bincount(tok[sel, 1].long(), minlength=V).float() / int(sel.sum())
+    assert (f1 - p[1]).abs().max() < 0.015, (f1, p[1])
+    assert set(tok[:, 0].tolist()) <= set(torch.nonzero(p[0] > 0).view(-1).tolist())
+
+
+def test_draws_are_reproducible_per_seed_and_position():
+    g = torch.Generator().manual_seed(3)
+    B, V = 8, 100
+    logits = torch.randn(B, 3, V, generator=g)
+    drafts = torch.randint(0, V, (B, 2), generator=g)
+    args = (logits, drafts, *_params(B, 1.0), torch.full((B,), 5), torch.arange(B) * 3)
+    a, b = sample_verify(*args), sample_verify(*args)
+    assert torch.equal(a[1], b[1]) and torch.equal(a[0], b[0])
+    u1 = uniform(torch.tensor([5]), torch.tensor([10]), 1, 1000)
+    u2 = uniform(torch.tensor([5]), torch.tensor([11]), 1, 1000)
+    u3 = uniform(torch.tensor([6]), torch.tensor([10]), 1, 1000)
+    assert not torch.equal(u1, u2) and not torch.equal(u1, u3)
+    assert 0 < float(u1.min()) and float(u1.max()) < 1 and abs(float(u1.mean()) - 0.5) < 0.05
