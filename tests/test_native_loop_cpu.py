@@ -52,10 +52,16 @@ class FakeRunner:
             d[-1] = (d[-1] + 1) % V
         return d
 
-    def prefill(self, prompts, bts, rows, st):
+    def prefill(self, prompts, bts, rows, st, sample=False):
         firsts = []
         for pr, r in zip(prompts, rows):
             t0 = f(pr[-1], len(pr) - 1)
+            if sample:                                     # the first token drawn as the GPU prefill does
+                from vllm_moet_b200.spec.device_sampler import sample_verify
+                i = torch.tensor([r])
+                t0 = int(sample_verify(self._onehot(t0)[None, None], torch.zeros(1, 0, dtype=torch.int32),
+                                       st.temperature[i], st.top_k[i], st.top_p[i], st.min_p[i], st.seed[i],
+                                       torch.tensor([len(pr) - 1]))[1][0, 0])
             st.tokens[r] = torch.tensor([t0] + self._drafts(t0, len(pr)), dtype=torch.int32)
             st.seq_pos[r] = len(pr)
             firsts.append(t0)
@@ -71,10 +77,12 @@ class FakeRunner:
         x[int(t)] = 10.0
         return x
 
-    def decode_body(self, st):
+    def decode_body(self, st, sample=False):
         self.steps += 1
         kp1 = self.k + 1
         lg = torch.zeros(st.B * kp1, V)
+        if sample:
+            return self._decode_sampled(st)
         for r in range(st.B):
             if not int(st.active[r]):
                 continue
@@ -91,6 +99,26 @@ class FakeRunner:
             st.tokens[r] = torch.tensor([nxt] + self._drafts(nxt, p + a + 1), dtype=torch.int32)
             st.seq_pos[r] = p + a + 1
         self.logits[st.B] = lg
+
+    def _decode_sampled(self, st):
+        """The sampling variant: the verify logits of the model, then the GPU runner's own
+        `_sample_verify` (the graph-safe sampler) and mtp_finalize's bookkeeping."""
+        from vllm_moet_b200.engine.gpu_runner import NativeRunner
+        kp1 = self.k + 1
+        lg = torch.zeros(st.B * kp1, V)
+        for r in range(st.B):
+            toks, p = st.tokens[r].tolist(), int(st.seq_pos[r])
+            for j in range(kp1):
+                lg[r * kp1 + j] = self._onehot(f(toks[j], p + j))
+        NativeRunner._sample_verify(self, st, lg)
+        self.logits[st.B] = lg
+        for r in range(st.B):
+            if not int(st.active[r]):
+                continue
+            a, p = int(st.n_acc[r]), int(st.seq_pos[r])
+            nxt = int(st.targets[r, a])
+            st.tokens[r] = torch.tensor([nxt] + self._drafts(nxt, p + a + 1), dtype=torch.int32)
+            st.seq_pos[r] = p + a + 1
 
     def main_logits(self, B):
         return self.logits.get(B)
@@ -245,3 +273,20 @@ def test_base_cache_misses_are_fetched_and_replayed(engine):
     assert [o.outputs[0].token_ids for o in out] == [chain([5, 6, 7], 9), chain([9, 9], 9)]
     assert llm.replay.stats["replayed_steps"] > 0 and cache.stats["fetched_rows"] > 0
     assert llm.kpi.snapshot()["replayed_steps"] == llm.replay.stats["replayed_steps"]
+
+
+def test_sampling_rows_share_the_batch_with_greedy_rows(engine):
+    """temperature > 0 on the GPU loop: the batch runs the sampling variant of the step;
+    greedy rows in it still decode the model's chain, a seeded sampling row is reproducible
+    and leaves the chain (T = 3 flattens the one-hot logits), and different seeds differ."""
+    def run(seed):
+        llm = engine()
+        sp_s = SamplingParams(max_tokens=12, ignore_eos=True, temperature=3.0, seed=seed)
+        sp_g = SamplingParams(max_tokens=12, ignore_eos=True)
+        out = llm.generate([[5, 6, 7], [9, 10]], [sp_g, sp_s])
+        return [o.outputs[0].token_ids for o in out]
+    g1, s1 = run(7)
+    g2, s2 = run(7)
+    _, s3 = run(8)
+    assert g1 == chain([5, 6, 7], 12) and g2 == g1
+    assert s1 == s2 and len(s1) == 12 and s1 != chain([9, 10], 12) and s3 != s1

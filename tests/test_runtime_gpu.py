@@ -152,3 +152,25 @@ def test_glm_head_dims_engine():
     finally:
         glm.ecfg.cuda_graphs = True
     glm.runner.check_status("glm dims")
+
+
+def test_sampling_variant_of_the_decode_graph(llm):
+    """temperature > 0 on one GPU: top-k 1 sampling is greedy decoding; a seeded request is
+    reproducible, graph and eager alike; a greedy row batched with a sampling row is
+    unchanged."""
+    prompts = [_prompt(40, 11), _prompt(60, 12)]
+    greedy = [o.outputs[0].token_ids for o in llm.generate(prompts, SamplingParams(max_tokens=16, ignore_eos=True))]
+    top1 = llm.generate(prompts, SamplingParams(max_tokens=16, ignore_eos=True, temperature=1.0, top_k=1))
+    assert [o.outputs[0].token_ids for o in top1] == greedy
+    sp = SamplingParams(max_tokens=16, ignore_eos=True, temperature=0.9, top_p=0.95, seed=5)
+    a = llm.generate([prompts[1]], sp)[0].outputs[0].token_ids
+    b = llm.generate([prompts[1]], sp)[0].outputs[0].token_ids
+    llm.ecfg.cuda_graphs = False
+    try:
+        c = llm.generate([prompts[1]], sp)[0].outputs[0].token_ids
+    finally:
+        llm.ecfg.cuda_graphs = True
+    assert a == b == c and len(a) == 16
+    mixed = llm.generate(prompts, [SamplingParams(max_tokens=16, ignore_eos=True), sp])
+    assert mixed[0].outputs[0].token_ids == greedy[0]
+    assert llm.runner.sample_graphs

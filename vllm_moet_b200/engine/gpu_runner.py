@@ -109,6 +109,7 @@ class NativeRunner:
         self.ws = self.ws_prefill
         self.scale = 1.0 / math.sqrt(cfg.qk_head_dim)
         self.graphs = {}
+        self.sample_graphs = {}       # bucket -> graph of the speculative-sampling decode step
         self.tp_group = None
         self.tp_rank, self.tp_size = mw.tp_rank, mw.tp_size
         self.ar = None            # fused peer-memory all-reduce (SymmAllReduce) for decode-sized steps
@@ -652,13 +653,14 @@ class NativeRunner:
 
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
-    def prefill(self, prompts: list, block_tables: list, seq_rows: list, state):
+    def prefill(self, prompts: list, block_tables: list, seq_rows: list, state, sample: bool = False):
         """Prefill whole prompts (one chunk each); fills main + MTP caches and the
         decode state rows `seq_rows` (tokens, positions, drafts).  Returns the
-        first generated token of each prompt."""
+        first generated token of each prompt.  `sample`: the first tokens are drawn with
+        the rows' sampling parameters (already set in `state`)."""
         self.ws = self.ws_prefill
         try:
-            out = self._prefill(prompts, block_tables, seq_rows, state)
+            out = self._prefill(prompts, block_tables, seq_rows, state, sample)
         finally:
             self.ws = self.ws_prefill
         self.check_status("prefill")
@@ -671,7 +673,7 @@ class NativeRunner:
             names = {1: "index out of range", 2: "bounded wait timed out", 3: "bad size", 4: "non-finite logits"}
             raise RuntimeError(f"device status {code} ({names.get(code, '?')}) during {where}")
 
-    def _prefill(self, prompts, block_tables, seq_rows, state):
+    def _prefill(self, prompts, block_tables, seq_rows, state, sample=False):
         dev, C = self.dev, self.C
         lens = [len(p) for p in prompts]
         T = sum(lens)
@@ -695,7 +697,15 @@ class NativeRunner:
         xl = x[last].contiguous()
         hid_last, logits = self._final(xl, None, "main")
         tgt = self.ws.get("pf.tgt", (len(prompts),), torch.int32)
-        self._argmax(logits, tgt)
+        if sample:
+            from ..spec.device_sampler import sample_verify
+            r = torch.tensor(seq_rows, dtype=torch.long, device=dev)
+            _, first = sample_verify(logits.view(B, 1, -1), torch.zeros(B, 0, dtype=torch.int32, device=dev),
+                                     state.temperature[r], state.top_k[r], state.top_p[r], state.min_p[r],
+                                     state.seed[r], torch.tensor(lens, dtype=torch.int32, device=dev) - 1)
+            tgt.copy_(first[:, 0])
+        else:
+            self._argmax(logits, tgt)
         if self.k == 0:
             state.set_rows(seq_rows, tgt, torch.tensor(lens, dtype=torch.int32, device=dev), None)
             self._pp_broadcast_state(state)
@@ -735,18 +745,32 @@ class NativeRunner:
             ws = self.ws_decode_by_bucket[B] = Workspace(self.dev)
         return ws
 
-    def decode_body(self, st):
+    def decode_body(self, st, sample: bool = False):
         """One MTP decode step over the device state `st` (all tensors static).
         Each batch bucket owns its workspace: a captured graph keeps the
-        addresses it was recorded with."""
+        addresses it was recorded with.  `sample`: verify with speculative sampling
+        (the state's per-row temperature / top-k / top-p / min-p / seed) instead of
+        greedy matching; rows at temperature 0 stay greedy."""
         prev = self.ws
         self.ws = self._bucket_ws(st.B)
         try:
-            self._decode_body(st)
+            self._decode_body(st, sample)
         finally:
             self.ws = prev
 
-    def _decode_body(self, st):
+    def _sample_verify(self, st, logits):
+        """Speculative sampling of the verify rows into targets / out_tokens / n_acc (the
+        outputs of argmax + mtp_accept), in graph-safe tensor ops."""
+        from ..spec.device_sampler import sample_verify
+        B, kp1 = st.B, self.k + 1
+        n, tok = sample_verify(logits.view(B, kp1, -1), st.tokens[:, 1:], st.temperature, st.top_k, st.top_p,
+                               st.min_p, st.seed, st.seq_pos)
+        n = n * st.active
+        st.targets.copy_(tok)
+        st.n_acc.copy_(n)
+        st.out_tokens.copy_(torch.where(st.arange_kp1[None, :] <= n[:, None], tok, torch.full_like(tok, -1)))
+
+    def _decode_body(self, st, sample: bool = False):
         C, k = self.C, self.k
         if self.cache is not None:
             self.miss.zero_()      # per-step miss count (read by the replay engine after the step)
@@ -764,8 +788,11 @@ class NativeRunner:
             self._pp_broadcast_state(st)
             return
         hid, logits = self._final(x, None, "main")
-        self._argmax(logits, st.targets.view(-1))
-        C.mtp_accept(st.targets, st.tokens, st.out_tokens, st.n_acc, st.active)
+        if sample:
+            self._sample_verify(st, logits)
+        else:
+            self._argmax(logits, st.targets.view(-1))
+            C.mtp_accept(st.targets, st.tokens, st.out_tokens, st.n_acc, st.active)
         if k == 0:
             st.seq_pos.add_(st.active)
             st.tokens.copy_(st.targets)
@@ -794,24 +821,25 @@ class NativeRunner:
         C.mtp_finalize(st.targets, st.n_acc, st.drafts, st.tokens, st.seq_pos, st.active)
         self._pp_broadcast_state(st)
 
-    def capture(self, st, warm: bool = True):
-        """Capture decode_body for the state's batch bucket (after one eager warm-up)."""
+    def capture(self, st, warm: bool = True, sample: bool = False):
+        """Capture decode_body for the state's batch bucket (after one eager warm-up);
+        the sampling variant is a second graph of the bucket (`sample_graphs`)."""
         if warm:
-            self.decode_body_eager_warm(st)
+            self.decode_body_eager_warm(st, sample)
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
             with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
-                self.decode_body(st)
+                self.decode_body(st, sample)
         torch.cuda.current_stream().wait_stream(s)
-        self.graphs[st.B] = g
+        (self.sample_graphs if sample else self.graphs)[st.B] = g
         self._bucket_ws(st.B).frozen = True
         return g
 
-    def decode_body_eager_warm(self, st):
+    def decode_body_eager_warm(self, st, sample: bool = False):
         snap = st.snapshot()
-        self.decode_body(st)
+        self.decode_body(st, sample)
         st.restore(snap)
         torch.cuda.synchronize()
 
@@ -835,6 +863,21 @@ class DecodeState:
         self.arange_b = torch.arange(B, dtype=torch.int32, device=dev)
         self.seq_rows = torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(kp1)
         self.active_rows = torch.zeros(B * kp1, dtype=torch.bool, device=dev)
+        # per-row sampling parameters (temperature 0 = greedy)
+        self.temperature = torch.zeros(B, dtype=torch.float32, device=dev)
+        self.top_k = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.top_p = torch.ones(B, dtype=torch.float32, device=dev)
+        self.min_p = torch.zeros(B, dtype=torch.float32, device=dev)
+        self.seed = torch.zeros(B, dtype=torch.int64, device=dev)
+
+    SAMPLING = ("temperature", "top_k", "top_p", "min_p", "seed")
+
+    def set_sampling(self, rows, temperature, top_k, top_p, min_p, seed):
+        """Host lists, one entry per row in `rows`."""
+        idx = torch.tensor(rows, dtype=torch.long)
+        for name, vals in zip(self.SAMPLING, (temperature, top_k, top_p, min_p, seed)):
+            t = getattr(self, name)
+            t[idx.to(t.device)] = torch.tensor(vals, dtype=t.dtype).to(t.device)
 
     def set_active(self, mask: torch.Tensor):
         self.active.copy_(mask.to(self.active.dtype))

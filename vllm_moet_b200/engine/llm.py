@@ -385,13 +385,14 @@ class LLM:
             raise NotImplementedError("logprobs under tensor parallelism: each rank holds a vocab shard")
         if sp.prompt_logprobs is not None and self.device.type == "cuda":
             raise NotImplementedError("prompt_logprobs: the GPU prefill keeps only each prompt's last logits")
-        if sp.temperature != 0 and self.device.type == "cuda":
-            raise NotImplementedError("temperature > 0: the GPU runner verifies drafts greedily inside the "
-                                      "decode graph; sampling is served by the CPU engine")
+        if sp.temperature != 0 and self.device.type == "cuda" and (self._tp_group is not None
+                                                                   or self._pp_group is not None):
+            raise NotImplementedError("temperature > 0 on the GPU runner: one GPU only so far (the sampler "
+                                      "needs whole-vocabulary logit rows; TP ranks hold vocab shards)")
         if sp.processes_logits or sp.min_p > 0:
-            if self.device.type == "cuda":
-                raise NotImplementedError("penalties / logit_bias / min_p: the GPU decode graph chooses tokens "
-                                          "from the raw logits; they are served by the CPU engine")
+            if self.device.type == "cuda" and sp.processes_logits:
+                raise NotImplementedError("penalties / logit_bias: the GPU decode graph chooses tokens from the "
+                                          "raw logits; they are served by the CPU engine")
             if getattr(self.runner, "sp_group", None) is not None or getattr(self.runner, "dspark", None):
                 raise NotImplementedError("penalties / logit_bias / min_p: not with SP prefill or DSpark drafting")
         if len(t) + sp.max_tokens + self.k + 1 > self.ecfg.max_model_len:
@@ -616,7 +617,7 @@ class LLM:
         keep their index; KV caches are paged, so only tokens / positions / block tables move)."""
         st2 = self._state(B_new)
         n = st.B
-        for name in ("tokens", "seq_pos", "block_table"):
+        for name in ("tokens", "seq_pos", "block_table") + tuple(getattr(st, "SAMPLING", ())):
             dst, src = getattr(st2, name), getattr(st, name)
             dst.zero_()
             dst[:n].copy_(src)
@@ -642,7 +643,6 @@ class LLM:
         rows: List[Optional[_Req]] = [None] * B
         steps = accepted = 0
         t_decode = 0.0
-        graph = runner.graphs.get(B) if self.ecfg.cuda_graphs else None
         bt_host = torch.zeros(B, self.max_blocks, dtype=torch.int32)
         while True:
             # serving: the batch may grow into a larger bucket, so offer room up to `cap` rows
@@ -661,7 +661,6 @@ class LLM:
                 bt_new = torch.zeros(B_new, self.max_blocks, dtype=torch.int32)
                 bt_new[:B] = bt_host
                 bt_host, B = bt_new, B_new
-                graph = runner.graphs.get(B) if self.ecfg.cuda_graphs else None
             free = [i for i, r in enumerate(rows) if r is None]
             adm = []
             while waiting and free and self.blocks.can_allocate(len(waiting[0].prompt) + waiting[0].params.max_tokens + kp1 + 1):
@@ -677,8 +676,10 @@ class LLM:
             if adm:
                 st.block_table.copy_(bt_host, non_blocking=False)
                 bts = [bt_host[r.row].tolist() for r in adm]
+                sample_pf = self._set_sampling(st, adm)
                 with self.timers.span("prefill") if self.timers is not None else contextlib.nullcontext():
-                    firsts = runner.prefill([r.prompt for r in adm], bts, [r.row for r in adm], st).tolist()
+                    firsts = runner.prefill([r.prompt for r in adm], bts, [r.row for r in adm], st,
+                                            **({"sample": True} if sample_pf else {})).tolist()
                 now = time.perf_counter()
                 want_lp = any(r.params.logprobs is not None for r in adm)
                 pl = runner.ws_prefill.get("main.logits", (len(adm), self.cfg.vocab), torch.float32) if want_lp \
@@ -693,8 +694,14 @@ class LLM:
             for i, on in enumerate(live):
                 pin_active[i] = 1 if on else 0
             st.set_active(pin_active.to(self.device, non_blocking=True))
-            if self.ecfg.cuda_graphs and graph is None:
-                graph = runner.capture(st)
+            # a batch with a sampling row runs the bucket's speculative-sampling variant
+            sample = any(r is not None and r.params.temperature > 0 for r in rows)
+            self._step_sample = sample
+            graph = None
+            if self.ecfg.cuda_graphs:
+                graph = (runner.sample_graphs if sample else runner.graphs).get(B)
+                if graph is None:
+                    graph = runner.capture(st, **({"sample": True} if sample else {}))
             t0 = time.perf_counter()
             if self.delta is not None:
                 self._delta_snap = st.snapshot()
@@ -702,7 +709,7 @@ class LLM:
                 self.cache.wait_idle()           # safe point: no pool / slot-table mutation in flight
                 self.cache.step_begin()
                 snap = st.snapshot()
-                step = graph.replay if graph is not None else (lambda: runner.decode_body(st))
+                step = graph.replay if graph is not None else (lambda: self._decode_eager(st))
                 f0 = self.cache.stats["fetched_rows"]
                 n_rep = self.replay.run(step, lambda: st.restore(snap), lambda: runner.route_ids(B))
                 self.cache.step_end()
@@ -711,7 +718,7 @@ class LLM:
             elif graph is not None:
                 graph.replay()
             else:
-                runner.decode_body(st)
+                self._decode_eager(st)
             if self.delta is not None:
                 self._delta_step(st, B, graph, kp1)
             if self.routing is not None:
@@ -735,6 +742,27 @@ class LLM:
                     self._finish_row(r, rows)
         self.stats = dict(steps=steps, accepted=accepted, decode_s=t_decode, bucket=B)
 
+    def _decode_eager(self, st):
+        if getattr(self, "_step_sample", False):
+            self.runner.decode_body(st, True)
+        else:
+            self.runner.decode_body(st)
+
+    def _set_sampling(self, st, adm) -> bool:
+        """Write the admitted rows' sampling parameters into the decode state (an unseeded
+        request gets a random seed) -> whether any of them samples."""
+        if not any(r.params.temperature > 0 for r in adm):
+            if hasattr(st, "set_sampling"):
+                st.set_sampling([r.row for r in adm], [0.0] * len(adm), [0] * len(adm), [1.0] * len(adm),
+                                [0.0] * len(adm), [0] * len(adm))
+            return False
+        import random
+        ps = [r.params for r in adm]
+        st.set_sampling([r.row for r in adm], [p.temperature for p in ps], [p.top_k for p in ps],
+                        [p.top_p for p in ps], [p.min_p for p in ps],
+                        [p.seed if p.seed is not None else random.getrandbits(62) for p in ps])
+        return True
+
     def _delta_step(self, st, B, graph, kp1):
         """After a decode step: feed routing to the delta tier's frequency policy and,
         with the confidence gate, promote this step's routed experts to FP4 and
@@ -748,7 +776,7 @@ class LLM:
         if self.gate is not None:
             rows = torch.nonzero(st.active_rows).flatten()
             logits = self.runner.main_logits(B)
-            step = (graph.replay if graph is not None else (lambda: self.runner.decode_body(st)))
+            step = (graph.replay if graph is not None else (lambda: self._decode_eager(st)))
             snap = self._delta_snap
 
             def run_step():
