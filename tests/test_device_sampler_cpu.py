@@ -67,3 +67,28 @@ def test_draws_are_reproducible_per_seed_and_position():
     u3 = uniform(torch.tensor([6]), torch.tensor([10]), 1, 1000)
     assert not torch.equal(u1, u2) and not torch.equal(u1, u3)
     assert 0 < float(u1.min()) and float(u1.max()) < 1 and abs(float(u1.mean()) - 0.5) < 0.05
+
+
+def _tp_sample(rank, world):
+    import torch.distributed as dist
+    from vllm_moet_b200.spec.device_sampler import gather_vocab
+    g = torch.Generator().manual_seed(4)
+    B, kp1, V = 4, 3, 48
+    logits = torch.randn(B * kp1, V, generator=g) * 2
+    drafts = torch.randint(0, V, (B, kp1 - 1), generator=g)
+    per = V // world
+    full = gather_vocab(logits[:, rank * per:(rank + 1) * per], dist.group.WORLD)
+    args = (drafts, *_params(B, 0.8, 7, 0.9), torch.arange(B) + 100, torch.arange(B) * 5)
+    got = sample_verify(full.view(B, kp1, V), *args)
+    want = sample_verify(logits.view(B, kp1, V), *args)
+    return torch.equal(full, logits), got[0].tolist(), got[1].tolist(), want[0].tolist(), want[1].tolist()
+
+
+def test_vocab_parallel_sampling_agrees_across_ranks():
+    """TP: the vocab shards gathered on every rank give the unsharded rows, so every rank
+    draws the tokens one rank would."""
+    from mp_util import run_ranks
+    res = run_ranks(_tp_sample, 2)
+    for same, n, tok, n_ref, tok_ref in res:
+        assert same and n == n_ref and tok == tok_ref
+    assert res[0][1:3] == res[1][1:3]

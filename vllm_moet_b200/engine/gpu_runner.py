@@ -700,7 +700,8 @@ class NativeRunner:
         if sample:
             from ..spec.device_sampler import sample_verify
             r = torch.tensor(seq_rows, dtype=torch.long, device=dev)
-            _, first = sample_verify(logits.view(B, 1, -1), torch.zeros(B, 0, dtype=torch.int32, device=dev),
+            _, first = sample_verify(self._full_vocab(logits).view(B, 1, -1),
+                                     torch.zeros(B, 0, dtype=torch.int32, device=dev),
                                      state.temperature[r], state.top_k[r], state.top_p[r], state.min_p[r],
                                      state.seed[r], torch.tensor(lens, dtype=torch.int32, device=dev) - 1)
             tgt.copy_(first[:, 0])
@@ -763,12 +764,22 @@ class NativeRunner:
         outputs of argmax + mtp_accept), in graph-safe tensor ops."""
         from ..spec.device_sampler import sample_verify
         B, kp1 = st.B, self.k + 1
+        logits = self._full_vocab(logits)
         n, tok = sample_verify(logits.view(B, kp1, -1), st.tokens[:, 1:], st.temperature, st.top_k, st.top_p,
                                st.min_p, st.seed, st.seq_pos)
         n = n * st.active
         st.targets.copy_(tok)
         st.n_acc.copy_(n)
         st.out_tokens.copy_(torch.where(st.arange_kp1[None, :] <= n[:, None], tok, torch.full_like(tok, -1)))
+
+    def _full_vocab(self, logits):
+        """Sampling under TP: the vocab shards of every rank, gathered (same rows everywhere)."""
+        if self.tp_group is None:
+            return logits
+        from ..spec.device_sampler import gather_vocab
+        R, Vl = logits.shape
+        buf = self.ws.get("smp.vocab", (self.tp_size, R, Vl), logits.dtype)
+        return gather_vocab(logits, self.tp_group, buf)
 
     def _decode_body(self, st, sample: bool = False):
         C, k = self.C, self.k

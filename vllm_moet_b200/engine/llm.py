@@ -385,10 +385,6 @@ class LLM:
             raise NotImplementedError("logprobs under tensor parallelism: each rank holds a vocab shard")
         if sp.prompt_logprobs is not None and self.device.type == "cuda":
             raise NotImplementedError("prompt_logprobs: the GPU prefill keeps only each prompt's last logits")
-        if sp.temperature != 0 and self.device.type == "cuda" and (self._tp_group is not None
-                                                                   or self._pp_group is not None):
-            raise NotImplementedError("temperature > 0 on the GPU runner: one GPU only so far (the sampler "
-                                      "needs whole-vocabulary logit rows; TP ranks hold vocab shards)")
         if sp.processes_logits or sp.min_p > 0:
             if self.device.type == "cuda" and sp.processes_logits:
                 raise NotImplementedError("penalties / logit_bias: the GPU decode graph chooses tokens from the "

@@ -25,7 +25,7 @@ is exact on every device.
 """
 from __future__ import annotations
 
-from typing import Tuple
+from typing import Optional, Tuple
 
 import torch
 
@@ -106,3 +106,15 @@ def sample_verify(logits: torch.Tensor, drafts: torch.Tensor, temperature: torch
     dpad = torch.cat([d, d.new_zeros(B, 1)], 1) if k else d.new_zeros(B, 1)
     tok = torch.where(j[None, :] < a[:, None], dpad, pick)
     return n_acc.int(), tok.int()
+
+
+def gather_vocab(logits: torch.Tensor, group, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Vocab-parallel logits [R, V/tp] (rank r holds ids [r V/tp, (r+1) V/tp)) -> the full
+    rows [R, V] on every rank (one all-gather).  Every rank then runs the same sampler on
+    the same rows with the same seeds, so all ranks draw the same tokens."""
+    import torch.distributed as dist
+    W = dist.get_world_size(group)
+    R, Vl = logits.shape
+    buf = (out if out is not None else logits.new_empty(W, R, Vl)).view(W * R, Vl)
+    dist.all_gather_into_tensor(buf, logits.contiguous(), group=group)
+    return buf.view(W, R, Vl).permute(1, 0, 2).reshape(R, W * Vl)
