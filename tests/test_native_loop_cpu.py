@@ -120,6 +120,10 @@ class FakeRunner:
             st.tokens[r] = torch.tensor([nxt] + self._drafts(nxt, p + a + 1), dtype=torch.int32)
             st.seq_pos[r] = p + a + 1
 
+    @staticmethod
+    def _full_vocab(logits):                               # one rank: the whole vocabulary
+        return logits
+
     def main_logits(self, B):
         return self.logits.get(B)
 
