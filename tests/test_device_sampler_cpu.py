@@ -92,3 +92,34 @@ def test_vocab_parallel_sampling_agrees_across_ranks():
     for same, n, tok, n_ref, tok_ref in res:
         assert same and n == n_ref and tok == tok_ref
     assert res[0][1:3] == res[1][1:3]
+
+
+def test_batched_processing_equals_per_row_processing():
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.spec.device_sampler import process_batch
+    from vllm_moet_b200.spec.logits_process import process_logits
+    g = torch.Generator().manual_seed(5)
+    B, kp1, V = 3, 3, 40
+    logits = torch.randn(B, kp1, V, generator=g) * 3
+    drafts = torch.randint(0, V, (B, kp1 - 1), generator=g)
+    sps = [SamplingParams(repetition_penalty=1.4, frequency_penalty=0.3, presence_penalty=0.1, logit_bias={3: 1.5}),
+           SamplingParams(),
+           SamplingParams(presence_penalty=-0.5, logit_bias={7: -2.0})]
+    prompts = [[1, 2, 3], [4, 5], [6, 6, 9]]
+    outs = [[3, 8, 8], [10], [9, 11]]
+    counts = torch.zeros(B, V)
+    mask = torch.zeros(B, V, dtype=torch.bool)
+    bias = torch.zeros(B, V)
+    for b in range(B):
+        for t in outs[b]:
+            counts[b, t] += 1
+        mask[b, prompts[b]] = True
+        for t, v in (sps[b].logit_bias or {}).items():
+            bias[b, t] = v
+    got = process_batch(logits, drafts, counts, mask, torch.tensor([p.repetition_penalty for p in sps]),
+                        torch.tensor([p.frequency_penalty for p in sps]), torch.tensor([p.presence_penalty for p in sps]),
+                        bias)
+    for b in range(B):
+        want = process_logits(logits[b], sps[b], prompts[b], outs[b], drafts[b].tolist())
+        assert torch.allclose(got[b], want, atol=1e-5), b
+    assert torch.equal(got[1], logits[1])

@@ -16,7 +16,7 @@ import torch
 
 from vllm_moet_b200 import SamplingParams
 from vllm_moet_b200.config import EngineConfig, MoetConfig, tiny_config
-from vllm_moet_b200.engine.gpu_runner import DecodeState
+from vllm_moet_b200.engine.gpu_runner import DecodeState, NativeRunner
 from vllm_moet_b200.engine.kv_manager import BlockManager
 from vllm_moet_b200.engine.llm import LLM
 from vllm_moet_b200.engine.tokenizer import ByteTokenizer
@@ -57,11 +57,8 @@ class FakeRunner:
         for pr, r in zip(prompts, rows):
             t0 = f(pr[-1], len(pr) - 1)
             if sample:                                     # the first token drawn as the GPU prefill does
-                from vllm_moet_b200.spec.device_sampler import sample_verify
-                i = torch.tensor([r])
-                t0 = int(sample_verify(self._onehot(t0)[None, None], torch.zeros(1, 0, dtype=torch.int32),
-                                       st.temperature[i], st.top_k[i], st.top_p[i], st.min_p[i], st.seed[i],
-                                       torch.tensor([len(pr) - 1]))[1][0, 0])
+                from vllm_moet_b200.engine.gpu_runner import NativeRunner
+                t0 = int(NativeRunner._sample_first(self, st, [r], self._onehot(t0)[None], [len(pr)])[0])
             st.tokens[r] = torch.tensor([t0] + self._drafts(t0, len(pr)), dtype=torch.int32)
             st.seq_pos[r] = len(pr)
             firsts.append(t0)
@@ -123,6 +120,8 @@ class FakeRunner:
     @staticmethod
     def _full_vocab(logits):                               # one rank: the whole vocabulary
         return logits
+
+    _process = staticmethod(NativeRunner._process)         # the GPU runner's own processing step
 
     def main_logits(self, B):
         return self.logits.get(B)
@@ -294,3 +293,21 @@ def test_sampling_rows_share_the_batch_with_greedy_rows(engine):
     _, s3 = run(8)
     assert g1 == chain([5, 6, 7], 12) and g2 == g1
     assert s1 == s2 and len(s1) == 12 and s1 != chain([9, 10], 12) and s3 != s1
+
+
+def test_penalties_in_the_gpu_loop(engine):
+    """Penalties / logit bias on the GPU loop: the sampling variant processes the verify
+    rows (drafts before row j count as generated) with device-side token counts kept by
+    the host loop; a repetition penalty breaks the fake model's repetition and a large
+    bias forces a token; greedy rows beside them keep the chain."""
+    llm = engine()
+    forced = SamplingParams(max_tokens=8, ignore_eos=True, logit_bias={77: 50.0})
+    out = llm.generate([[5, 6, 7], [9, 10]], [SamplingParams(max_tokens=8, ignore_eos=True), forced])
+    assert out[0].outputs[0].token_ids == chain([5, 6, 7], 8)
+    assert out[1].outputs[0].token_ids == [77] * 8
+    st = llm._states[2]
+    assert st.proc is not None and float(st.proc["counts"][1, 77]) == 8.0
+    # presence penalty 2 against a bias of 1.5 on token 77: once generated, 77 loses to the model
+    pen = SamplingParams(max_tokens=6, ignore_eos=True, logit_bias={77: 11.0}, presence_penalty=2.0)
+    got = llm.generate([[9, 10]], pen)[0].outputs[0].token_ids
+    assert got[0] == 77 and 77 not in got[1:]

@@ -698,13 +698,7 @@ class NativeRunner:
         hid_last, logits = self._final(xl, None, "main")
         tgt = self.ws.get("pf.tgt", (len(prompts),), torch.int32)
         if sample:
-            from ..spec.device_sampler import sample_verify
-            r = torch.tensor(seq_rows, dtype=torch.long, device=dev)
-            _, first = sample_verify(self._full_vocab(logits).view(B, 1, -1),
-                                     torch.zeros(B, 0, dtype=torch.int32, device=dev),
-                                     state.temperature[r], state.top_k[r], state.top_p[r], state.min_p[r],
-                                     state.seed[r], torch.tensor(lens, dtype=torch.int32, device=dev) - 1)
-            tgt.copy_(first[:, 0])
+            tgt.copy_(self._sample_first(state, seq_rows, logits, lens))
         else:
             self._argmax(logits, tgt)
         if self.k == 0:
@@ -764,13 +758,37 @@ class NativeRunner:
         outputs of argmax + mtp_accept), in graph-safe tensor ops."""
         from ..spec.device_sampler import sample_verify
         B, kp1 = st.B, self.k + 1
-        logits = self._full_vocab(logits)
-        n, tok = sample_verify(logits.view(B, kp1, -1), st.tokens[:, 1:], st.temperature, st.top_k, st.top_p,
+        logits = self._full_vocab(logits).view(B, kp1, -1)
+        if st.proc is not None:               # penalties / logit bias, verify row j after drafts[:j]
+            logits = self._process(st, logits, st.tokens[:, 1:], None)
+        n, tok = sample_verify(logits, st.tokens[:, 1:], st.temperature, st.top_k, st.top_p,
                                st.min_p, st.seed, st.seq_pos)
         n = n * st.active
         st.targets.copy_(tok)
         st.n_acc.copy_(n)
         st.out_tokens.copy_(torch.where(st.arange_kp1[None, :] <= n[:, None], tok, torch.full_like(tok, -1)))
+
+    @staticmethod
+    def _process(st, logits, drafts, rows):
+        from ..spec.device_sampler import process_batch
+        pr = st.proc
+        sel = (lambda t: t) if rows is None else (lambda t: t[rows])
+        return process_batch(logits, drafts, sel(pr["counts"]), sel(pr["prompt_mask"]), sel(pr["repetition"]),
+                             sel(pr["frequency"]), sel(pr["presence"]), sel(pr["bias"]))
+
+    def _sample_first(self, state, seq_rows, logits, lens):
+        """First generated tokens drawn with the rows' sampling / processing parameters."""
+        from ..spec.device_sampler import sample_verify
+        dev = logits.device
+        B = len(seq_rows)
+        r = torch.tensor(seq_rows, dtype=torch.long, device=dev)
+        x = self._full_vocab(logits).view(B, 1, -1)
+        none = torch.zeros(B, 0, dtype=torch.int32, device=dev)
+        if state.proc is not None:
+            x = self._process(state, x, none, r)
+        _, first = sample_verify(x, none, state.temperature[r], state.top_k[r], state.top_p[r], state.min_p[r],
+                                 state.seed[r], torch.tensor(lens, dtype=torch.int32, device=dev) - 1)
+        return first[:, 0]
 
     def _full_vocab(self, logits):
         """Sampling under TP: the vocab shards of every rank, gathered (same rows everywhere)."""
@@ -881,7 +899,48 @@ class DecodeState:
         self.min_p = torch.zeros(B, dtype=torch.float32, device=dev)
         self.seed = torch.zeros(B, dtype=torch.int64, device=dev)
 
+        self.proc = None      # penalty / logit-bias tensors, allocated by the first request that needs them
+
     SAMPLING = ("temperature", "top_k", "top_p", "min_p", "seed")
+
+    def ensure_processing(self, vocab: int):
+        if self.proc is None:
+            dev, B = self.tokens.device, self.B
+            self.proc = dict(counts=torch.zeros(B, vocab, dtype=torch.float32, device=dev),
+                             prompt_mask=torch.zeros(B, vocab, dtype=torch.bool, device=dev),
+                             repetition=torch.ones(B, dtype=torch.float32, device=dev),
+                             frequency=torch.zeros(B, dtype=torch.float32, device=dev),
+                             presence=torch.zeros(B, dtype=torch.float32, device=dev),
+                             bias=torch.zeros(B, vocab, dtype=torch.float32, device=dev))
+        return self.proc
+
+    def set_processing(self, row: int, prompt, params):
+        """Reset row `row` for a new request: its prompt tokens, penalties and bias."""
+        pr, dev = self.proc, self.tokens.device
+        V = pr["counts"].shape[1]
+        pr["counts"][row].zero_()
+        pr["prompt_mask"][row].zero_()
+        pr["bias"][row].zero_()
+        ids = torch.tensor([t for t in prompt if 0 <= t < V], dtype=torch.long)
+        if len(ids):
+            pr["prompt_mask"][row, ids.to(dev)] = True
+        pr["repetition"][row] = float(params.repetition_penalty)
+        pr["frequency"][row] = float(params.frequency_penalty)
+        pr["presence"][row] = float(params.presence_penalty)
+        if params.logit_bias:
+            b = {t: v for t, v in params.logit_bias.items() if 0 <= t < V}
+            if b:
+                pr["bias"][row, torch.tensor(list(b), dtype=torch.long).to(dev)] = \
+                    torch.tensor(list(b.values()), dtype=torch.float32).to(dev)
+
+    def count_tokens(self, rows, tokens):
+        """Generated tokens of the last step (host lists) into the rows' counts."""
+        if self.proc is None or not rows:
+            return
+        dev = self.tokens.device
+        r = torch.tensor(rows, dtype=torch.long)
+        t = torch.tensor(tokens, dtype=torch.long)
+        self.proc["counts"].index_put_((r.to(dev), t.to(dev)), torch.ones(len(rows), device=dev), accumulate=True)
 
     def set_sampling(self, rows, temperature, top_k, top_p, min_p, seed):
         """Host lists, one entry per row in `rows`."""

@@ -386,9 +386,6 @@ class LLM:
         if sp.prompt_logprobs is not None and self.device.type == "cuda":
             raise NotImplementedError("prompt_logprobs: the GPU prefill keeps only each prompt's last logits")
         if sp.processes_logits or sp.min_p > 0:
-            if self.device.type == "cuda" and sp.processes_logits:
-                raise NotImplementedError("penalties / logit_bias: the GPU decode graph chooses tokens from the "
-                                          "raw logits; they are served by the CPU engine")
             if getattr(self.runner, "sp_group", None) is not None or getattr(self.runner, "dspark", None):
                 raise NotImplementedError("penalties / logit_bias / min_p: not with SP prefill or DSpark drafting")
         if len(t) + sp.max_tokens + self.k + 1 > self.ecfg.max_model_len:
@@ -617,6 +614,10 @@ class LLM:
             dst, src = getattr(st2, name), getattr(st, name)
             dst.zero_()
             dst[:n].copy_(src)
+        if getattr(st, "proc", None) is not None:
+            pr2 = st2.ensure_processing(st.proc["counts"].shape[1])
+            for name, src in st.proc.items():
+                pr2[name][:n].copy_(src)
         return st2
 
     @staticmethod
@@ -680,6 +681,8 @@ class LLM:
                 want_lp = any(r.params.logprobs is not None for r in adm)
                 pl = runner.ws_prefill.get("main.logits", (len(adm), self.cfg.vocab), torch.float32) if want_lp \
                     else None
+                if getattr(st, "proc", None) is not None:
+                    st.count_tokens([r.row for r in adm], firsts)
                 for j, (r, f) in enumerate(zip(adm, firsts)):
                     r.t_first = now
                     if self._emit(r, [f], pl[j:j + 1] if pl is not None else None):
@@ -691,7 +694,7 @@ class LLM:
                 pin_active[i] = 1 if on else 0
             st.set_active(pin_active.to(self.device, non_blocking=True))
             # a batch with a sampling row runs the bucket's speculative-sampling variant
-            sample = any(r is not None and r.params.temperature > 0 for r in rows)
+            sample = any(r is not None and (r.params.temperature > 0 or r.params.processes_logits) for r in rows)
             self._step_sample = sample
             graph = None
             if self.ecfg.cuda_graphs:
@@ -728,6 +731,14 @@ class LLM:
             steps += 1
             dl = runner.main_logits(B) if any(r is not None and r.params.logprobs is not None for r in rows) \
                 else None
+            if getattr(st, "proc", None) is not None:          # generated-token counts for the penalties
+                cr, ct = [], []
+                for i, r in enumerate(rows):
+                    if r is not None:
+                        n_i = int(pin_acc[i]) + 1
+                        cr += [i] * n_i
+                        ct += pin_out[i, :n_i].tolist()
+                st.count_tokens(cr, ct)
             for i, r in enumerate(rows):
                 if r is None:
                     continue
@@ -747,7 +758,14 @@ class LLM:
     def _set_sampling(self, st, adm) -> bool:
         """Write the admitted rows' sampling parameters into the decode state (an unseeded
         request gets a random seed) -> whether any of them samples."""
-        if not any(r.params.temperature > 0 for r in adm):
+        if hasattr(st, "ensure_processing"):
+            # the state's processing tensors exist before its sampling-variant graph is captured
+            if any(r.params.processes_logits or r.params.temperature > 0 for r in adm):
+                st.ensure_processing(self.cfg.vocab)
+            if st.proc is not None:
+                for r in adm:
+                    st.set_processing(r.row, r.prompt, r.params)
+        if not any(r.params.temperature > 0 or r.params.processes_logits for r in adm):
             if hasattr(st, "set_sampling"):
                 st.set_sampling([r.row for r in adm], [0.0] * len(adm), [0] * len(adm), [1.0] * len(adm),
                                 [0.0] * len(adm), [0] * len(adm))

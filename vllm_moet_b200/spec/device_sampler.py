@@ -118,3 +118,27 @@ def gather_vocab(logits: torch.Tensor, group, out: Optional[torch.Tensor] = None
     buf = (out if out is not None else logits.new_empty(W, R, Vl)).view(W * R, Vl)
     dist.all_gather_into_tensor(buf, logits.contiguous(), group=group)
     return buf.view(W, R, Vl).permute(1, 0, 2).reshape(R, W * Vl)
+
+
+def process_batch(logits: torch.Tensor, drafts: torch.Tensor, counts: torch.Tensor, prompt_mask: torch.Tensor,
+                  repetition: torch.Tensor, frequency: torch.Tensor, presence: torch.Tensor,
+                  bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Penalties and logit bias of a decode batch in tensor ops (the batched form of
+    ``logits_process.process_logits``).  logits [B, k+1, V]; drafts [B, k]; counts [B, V]
+    (f32 counts of each row's generated tokens so far); prompt_mask [B, V] (bool);
+    per-row repetition / frequency / presence [B]; bias [B, V] or None.  Verify row j sees
+    the drafts before it as generated.  Rows with neutral parameters come out unchanged."""
+    B, kp1, V = logits.shape
+    c = counts[:, None, :].expand(B, kp1, V)
+    if kp1 > 1:
+        inc = torch.zeros(B, kp1, V, dtype=counts.dtype, device=counts.device)
+        inc[:, 1:].scatter_(-1, drafts.long()[..., None], 1.0)
+        c = c + torch.cumsum(inc, dim=1)
+    x = logits.float()
+    r = repetition.float()[:, None, None]
+    seen = (c > 0) | prompt_mask[:, None, :]
+    x = torch.where(seen, torch.where(x > 0, x / r, x * r), x)
+    x = x - frequency.float()[:, None, None] * c - presence.float()[:, None, None] * (c > 0).float()
+    if bias is not None:
+        x = x + bias[:, None, :]
+    return x
