@@ -32,8 +32,11 @@ def test_calibration_projected_to_valid_prefix():
 
 def test_budget_prefers_confident_requests():
     surv = torch.tensor([[0.9, 0.9, 0.9, 0.9], [0.5, 0.4, 0.3, 0.2]])
-    w = allocate_widths(surv, torch.ones(4), num_reqs=2, length=4, tau=0.1, budget_frac=0.5)
+    w = allocate_widths(surv, torch.ones(4), num_reqs=2, length=4, tau=0.0, budget_frac=0.5)
     assert w.tolist() == [4, 0]
+    # tau > 0 is a static confidence width per request, without a budget
+    w = allocate_widths(surv, torch.ones(4), num_reqs=2, length=4, tau=0.35, budget_frac=0.5)
+    assert w.tolist() == [4, 2]
 
 
 def test_greedy_accept_valid_len():

@@ -23,9 +23,14 @@ class TorchRunner:
         if dspark is not None:
             from ..spec.dspark import DSparkDrafter
             torch.manual_seed(dspark.get("seed", 0))
+            from ..spec.dspark_policy import DSparkPolicy
+            block = dspark.get("block", 4)
             self.dspark = dict(drafter=dspark.get("drafter") or DSparkDrafter(mw.cfg.hidden, mw.cfg.vocab,
-                                                                               block=dspark.get("block", 4)),
+                                                                               block=block),
                                tau=dspark.get("tau", 0.5), budget_frac=dspark.get("budget_frac", 0.5))
+            # hardware-aware verify length: a cost table T(R, L) given, or profiled here
+            pol = DSparkPolicy(block, self.dspark["tau"], self.dspark["budget_frac"])
+            self.dspark["policy"] = pol
         self.dev = torch.device(device)
         self.cs = ref.rope_cos_sin(mw.cfg, max_len + 64, self.dev)
         self.rows = {}
@@ -44,6 +49,12 @@ class TorchRunner:
         self.dcp_group = dcp_group      # decode-context-parallel ranks: KV interleaved by position, LSE merge
         self.dcp_interleave = dcp_interleave
         self.ep_group = ep_group        # expert parallelism over data-parallel ranks (all-to-all MoE)
+        if dspark is not None:
+            if dspark.get("cost_table") is not None:
+                pol.set_cost_table(*dspark["cost_table"])
+            elif dspark.get("profile"):
+                pol.set_cost_table(dspark.get("r_grid", [1, 2, 4]),
+                                   self.profile_dspark(dspark.get("r_grid", [1, 2, 4]), block))
 
     def _row(self, r):
         return self.rows[r]
@@ -231,18 +242,19 @@ class TorchRunner:
             return self._step(rows)
 
     def _dspark_step(self, rows):
-        """DSpark: one parallel block proposal per live row, widths from the batch-wide
-        verify budget (`allocate_widths`), then each row verifies [pending token] +
-        drafts[:width] in one target pass and emits the accepted prefix + the correction."""
-        from ..spec.dspark import allocate_widths
+        """DSpark: the policy picks the batch-uniform verify length L (tokens / s from the
+        cost table, calibrated survival and the engine overhead); one parallel block
+        proposal per live row; per-row widths inside L (`allocate_widths`); each row
+        verifies [pending token] + drafts[:width] in one target pass and emits the
+        accepted prefix + the correction; the outcome feeds survival calibration."""
         ds = self.dspark
-        drafter = ds["drafter"]
+        drafter, pol = ds["drafter"], ds["policy"]
+        L = pol.begin_step(len(rows))
         h = torch.stack([self.rows[r]["hid"].float() for r in rows])
         last = torch.tensor([self.rows[r]["tokens"][0] for r in rows], device=self.dev)
         drafts, _, surv = drafter.propose(h, last)
-        L = drafts.shape[1]
-        widths = allocate_widths(surv, torch.ones(L), len(rows), L, ds["tau"], ds["budget_frac"])
-        out = {}
+        widths = pol.allocate(surv, len(rows), L) if L > 0 else torch.zeros(len(rows), dtype=torch.int32)
+        out, acc = {}, []
         for i, r in enumerate(rows):
             st = self.rows[r]
             p, w = st["pos"], int(widths[i])
@@ -257,7 +269,32 @@ class TorchRunner:
             self.last_logits[r] = logits[: a + 1]
             st["tokens"], st["pos"], st["hid"] = [tg[a]], p + a + 1, hid[a]
             out[r] = (tg[: a + 1], a)
+            acc.append(a)
+        pol.observe(surv, widths, torch.tensor(acc), L)
         return out
+
+    @torch.no_grad()
+    def profile_dspark(self, r_grid, gamma: int, context: int = 16):
+        """The DSpark cost table of this engine: seconds of one verify step of R rows at
+        width 1 + L (a row verifies in one target pass of 1 + L tokens after `context`)."""
+        from ..spec.dspark_policy import profile_cost_table
+        H = self.mw.cfg.hidden
+        caches = {}
+
+        def step(R, L):
+            for i in range(R):
+                kv = caches.get(i)
+                if kv is None:
+                    kv = caches[i] = ref.RefKV(len(self.mw.layers))
+                    ref.forward(self.mw, torch.arange(3, 3 + context, device=self.dev),
+                                torch.arange(context, device=self.dev), self.cs, kv)
+                kv.truncate(context)
+                ref.forward(self.mw, torch.full((L + 1,), 5, device=self.dev),
+                            torch.arange(context, context + L + 1, device=self.dev), self.cs, kv)
+            self.dspark["drafter"].propose(torch.zeros(R, H, device=self.dev),
+                                           torch.zeros(R, dtype=torch.long, device=self.dev))
+        with self._ctx():
+            return profile_cost_table(step, r_grid, gamma, repeats=3)
 
     def _step(self, rows):
         if self.dspark is not None:

@@ -8,12 +8,13 @@ block is coherent without L sequential backbone passes.  A **survival head**
 predicts, per position, the probability that the draft survives
 verification.
 
-:func:`allocate_widths` is the hardware-aware scheduler: calibrated survival
-scores (survival x per-position calibration) are projected to a valid prefix
-with a running minimum, positions above ``tau`` become candidates, and a
-global verify budget (``budget_frac`` x requests x length tokens) keeps the
-best-scored candidates -- ties broken by position, then request, so a tie
-never inflates the budget and every request's width is a prefix.
+:func:`allocate_widths` gives each request its verify width from calibrated
+survival scores (survival x per-position calibration, projected to a valid
+prefix with a running minimum): a static confidence threshold ``tau``, or with
+``tau`` = 0 a global budget (``budget_frac`` x requests x length tokens) spent on
+the best scores, ties to earlier positions and requests, so a tie never
+inflates the budget and every width is a prefix.  The hardware-aware choice of
+the batch-wide verify length lives in :mod:`.dspark_policy`.
 Reference: DSpark drafter and scheduler, patch P:14478-14971 and the tests at
 P:753-800.
 """
@@ -27,25 +28,28 @@ import torch.nn as nn
 
 def allocate_widths(survival: torch.Tensor, calibration: torch.Tensor, num_reqs: int, length: int,
                     tau: float, budget_frac: float) -> torch.Tensor:
-    """survival [>=num_reqs, >=length], calibration [>=length] -> int32 widths [num_reqs] (<= length)."""
-    s = survival[:num_reqs, :length].float() * calibration[:length].float()[None, :]
-    s = torch.cummin(s, dim=1).values                     # valid-prefix projection
-    cand = s > tau
-    budget = int(budget_frac * num_reqs * length + 1e-9)
-    if budget <= 0:
-        return torch.zeros(num_reqs, dtype=torch.int32)
-    r_idx, p_idx = cand.nonzero(as_tuple=True)
-    if r_idx.numel() > budget:
-        scores = s[r_idx, p_idx]
-        # sort by score desc, then position asc, then request asc (stable lexicographic)
-        order = sorted(range(r_idx.numel()), key=lambda i: (-float(scores[i]), int(p_idx[i]), int(r_idx[i])))
-        keep = torch.zeros_like(cand)
-        for i in order[:budget]:
-            keep[r_idx[i], p_idx[i]] = True
-        cand = keep
-    # a width is the length of the selected prefix
-    widths = torch.cumprod(cand.int(), dim=1).sum(dim=1)
-    return widths.to(torch.int32)
+    """survival [>=num_reqs, >=length], calibration [>=length] -> int32 widths [num_reqs] (<= length).
+
+    Scores are survival x calibration, projected onto a non-increasing curve (running
+    minimum) so every selection is a prefix.  tau > 0: each request keeps the positions
+    scoring >= tau (a static confidence width).  tau = 0: a global budget of
+    budget_frac x requests x length positions goes to the best scores; the flattened
+    rows are sorted stably, so equal scores go to earlier positions and requests and
+    the budget is used exactly."""
+    s = survival[:num_reqs, :length].float() * calibration[:length].float().to(survival.device)[None, :]
+    s = torch.cummin(s, dim=1).values
+    if tau > 0:
+        return (s >= tau).sum(dim=1, dtype=torch.int32).clamp_max(length)
+    budget = min(max(int(num_reqs * length * budget_frac + 1e-9), 0), num_reqs * length)
+    if budget == 0:
+        return torch.zeros(num_reqs, dtype=torch.int32, device=s.device)
+    if budget == num_reqs * length:
+        return torch.full((num_reqs,), length, dtype=torch.int32, device=s.device)
+    # positions in (request, position) order; a non-increasing row keeps its prefix first
+    order = torch.sort(s.reshape(-1), descending=True, stable=True).indices
+    keep = torch.zeros(num_reqs * length, dtype=torch.bool, device=s.device)
+    keep[order[:budget]] = True
+    return keep.view(num_reqs, length).sum(dim=1, dtype=torch.int32)
 
 
 class DSparkDrafter(nn.Module):
@@ -76,7 +80,8 @@ class DSparkDrafter(nn.Module):
         -> (drafts [R, L], draft probs [R, L, V], survival [R, L])."""
         z = self.backbone(h)
         base = self.head(z)                                # [R, L, V]
-        surv = torch.sigmoid(self.survival(z)).squeeze(-1)
+        # survival of position j = probability that drafts 1..j all survive (a cumulative product)
+        surv = torch.cumprod(torch.sigmoid(self.survival(z)).squeeze(-1), dim=1)
         prev = last_token
         drafts, probs = [], []
         for j in range(self.block):                        # cheap sequential Markov walk
