@@ -279,7 +279,7 @@ def test_hyper_connections_engine_matches_oracle():
     assert llm.runner.prefix_stats["hits"] == 1
     assert outs[0] != plain.generate([prompts[0]], sp)[0].outputs[0].token_ids
     with pytest.raises(NotImplementedError):
-        LLM("tiny-moe", device="cpu", hc_mult=4, speculative_method="dspark")
+        LLM("tiny-moe", device="cpu", hc_mult=4, speculative_method="dspark", dspark={"model": "simple"})
 
 
 def test_chunked_prefill_interleaves_with_decode():

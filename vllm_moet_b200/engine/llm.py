@@ -87,9 +87,11 @@ class LLM:
         if cfg.hc_mult > 1 and self.device.type == "cuda":
             raise NotImplementedError("hyper-connections (hc_mult > 1) run on the CPU engine; the GPU layer kernels "
                                       "keep one residual stream")
-        if cfg.hc_mult > 1 and (sp_group is not None or speculative_method == "dspark"):
-            raise NotImplementedError("hyper-connections: not with SP prefill or DSpark drafting (both read a "
-                                      "single-stream hidden state)")
+        simple_dspark = speculative_method == "dspark" and ((dspark or {}).get("model", "context") != "context"
+                                                            or (dspark or {}).get("drafter") is not None)
+        if cfg.hc_mult > 1 and (sp_group is not None or simple_dspark):
+            raise NotImplementedError("hyper-connections: not with SP prefill or a context-free DSpark drafter "
+                                      "(both read a single-stream hidden state)")
         self._chunk_budget = None
         if enable_chunked_prefill:
             if self.device.type == "cuda":

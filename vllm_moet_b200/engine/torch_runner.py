@@ -25,9 +25,13 @@ class TorchRunner:
             torch.manual_seed(dspark.get("seed", 0))
             from ..spec.dspark_policy import DSparkPolicy
             block = dspark.get("block", 4)
-            self.dspark = dict(drafter=dspark.get("drafter") or DSparkDrafter(mw.cfg.hidden, mw.cfg.vocab,
-                                                                               block=block),
-                               tau=dspark.get("tau", 0.5), budget_frac=dspark.get("budget_frac", 0.5))
+            # drafter: "context" (the DSpark draft model over the target's aux hidden states,
+            # default), "simple" (a context-free block head), or an object given as "drafter"
+            drafter = dspark.get("drafter")
+            if drafter is None and dspark.get("model", "context") == "simple":
+                drafter = DSparkDrafter(mw.cfg.hidden, mw.cfg.vocab, block=block)
+            self.dspark = dict(drafter=drafter, tau=dspark.get("tau", 0.5),
+                               budget_frac=dspark.get("budget_frac", 0.5))
             # hardware-aware verify length: a cost table T(R, L) given, or profiled here
             pol = DSparkPolicy(block, self.dspark["tau"], self.dspark["budget_frac"])
             self.dspark["policy"] = pol
@@ -50,6 +54,11 @@ class TorchRunner:
         self.dcp_interleave = dcp_interleave
         self.ep_group = ep_group        # expert parallelism over data-parallel ranks (all-to-all MoE)
         if dspark is not None:
+            if self.dspark["drafter"] is None:
+                from ..models.dspark_model import DSparkModelDrafter, random_dspark_weights
+                dw = random_dspark_weights(mw, num_layers=dspark.get("layers", 2), window=dspark.get("window", 128),
+                                           seed=dspark.get("seed", 0))
+                self.dspark["drafter"] = DSparkModelDrafter(mw, dw, block, self.cs)
             if dspark.get("cost_table") is not None:
                 pol.set_cost_table(*dspark["cost_table"])
             elif dspark.get("profile"):
@@ -134,8 +143,13 @@ class TorchRunner:
         prompt, main, mtp = st["prompt"], st["main"], st["mtp"]
         n, s = len(prompt), st["done"]
         e = min(n, s + max(1, budget))
+        cd = self._context_drafter()
+        aux = cd.aux_request() if cd is not None else None
         ls, hs = ref.forward(self.mw, torch.tensor(prompt[s:e], device=self.dev),
-                             torch.arange(s, e, device=self.dev), self.cs, main)
+                             torch.arange(s, e, device=self.dev), self.cs, main, aux=aux)
+        if cd is not None:
+            st.setdefault("dctx", cd.new_context())
+            cd.extend(st["dctx"], aux, s, e - s)
         st["logits"].append(ls)
         st["chunks"] += 1
         b = self.prefix_block
@@ -164,7 +178,7 @@ class TorchRunner:
         for m, h in st["bound"].items():
             self._prefix_put(prompt[:m], main, mtp, h, logits[:m])
         self.rows[r] = dict(main=main, mtp=mtp, tokens=[tgt] + drafts, pos=n, sample=smp, hid=hid[-1],
-                            sp=st["sp"], prompt=prompt, out=[tgt])
+                            sp=st["sp"], prompt=prompt, out=[tgt], dctx=st.get("dctx"))
         del self.partial[r]
         return tgt
 
@@ -208,9 +222,15 @@ class TorchRunner:
         c.k, c.v = list(kv.k), list(kv.v)        # later appends concatenate into new tensors
         return c
 
+    def _context_drafter(self):
+        d = self.dspark["drafter"] if self.dspark is not None else None
+        return d if hasattr(d, "extend") else None
+
     def _prefix_lookup(self, prompt):
-        """-> (m, entry) of the longest cached block-aligned prefix shorter than the prompt."""
-        if not self.prefix_block or self.sp_group is not None or self.dcp_group is not None:
+        """-> (m, entry) of the longest cached block-aligned prefix shorter than the prompt.
+        (Not with a context drafter: its context K/V of the prefix are not cached.)"""
+        if not self.prefix_block or self.sp_group is not None or self.dcp_group is not None or \
+                self._context_drafter() is not None:
             return 0, None
         self.prefix_stats["lookups"] += 1
         b = self.prefix_block
@@ -250,9 +270,15 @@ class TorchRunner:
         ds = self.dspark
         drafter, pol = ds["drafter"], ds["policy"]
         L = pol.begin_step(len(rows))
-        h = torch.stack([self.rows[r]["hid"].float() for r in rows])
-        last = torch.tensor([self.rows[r]["tokens"][0] for r in rows], device=self.dev)
-        drafts, _, surv = drafter.propose(h, last)
+        cd = self._context_drafter()
+        if cd is not None:
+            props = [cd.propose_one(self.rows[r]["dctx"], self.rows[r]["tokens"][0], self.rows[r]["pos"])
+                     for r in rows]
+            drafts, surv = torch.stack([d for d, _, _ in props]), torch.stack([c for _, _, c in props])
+        else:
+            h = torch.stack([self.rows[r]["hid"].float() for r in rows])
+            last = torch.tensor([self.rows[r]["tokens"][0] for r in rows], device=self.dev)
+            drafts, _, surv = drafter.propose(h, last)
         widths = pol.allocate(surv, len(rows), L) if L > 0 else torch.zeros(len(rows), dtype=torch.int32)
         out, acc = {}, []
         for i, r in enumerate(rows):
@@ -260,12 +286,15 @@ class TorchRunner:
             p, w = st["pos"], int(widths[i])
             st["main"].truncate(p)
             toks = torch.tensor([st["tokens"][0]] + drafts[i, :w].tolist(), device=self.dev)
+            aux = cd.aux_request() if cd is not None else None
             logits, hid = ref.forward(self.mw, toks, torch.arange(p, p + w + 1, device=self.dev), self.cs,
-                                      st["main"])
+                                      st["main"], aux=aux)
             tg = logits.argmax(-1).tolist()
             a = 0
             while a < w and int(drafts[i, a]) == tg[a]:
                 a += 1
+            if cd is not None:                         # the verified positions p .. p + a join the context
+                cd.extend(st["dctx"], aux, p, a + 1)
             self.last_logits[r] = logits[: a + 1]
             st["tokens"], st["pos"], st["hid"] = [tg[a]], p + a + 1, hid[a]
             out[r] = (tg[: a + 1], a)
@@ -291,8 +320,16 @@ class TorchRunner:
                 kv.truncate(context)
                 ref.forward(self.mw, torch.full((L + 1,), 5, device=self.dev),
                             torch.arange(context, context + L + 1, device=self.dev), self.cs, kv)
-            self.dspark["drafter"].propose(torch.zeros(R, H, device=self.dev),
-                                           torch.zeros(R, dtype=torch.long, device=self.dev))
+            cd = self._context_drafter()
+            if cd is not None:
+                for i in range(R):
+                    c = cd.new_context()
+                    cd.extend(c, {li: torch.zeros(context, H, device=self.dev) for li in cd.dw.target_layers},
+                              0, context)
+                    cd.propose_one(c, 5, context)
+            else:
+                self.dspark["drafter"].propose(torch.zeros(R, H, device=self.dev),
+                                               torch.zeros(R, dtype=torch.long, device=self.dev))
         with self._ctx():
             return profile_cost_table(step, r_grid, gamma, repeats=3)
 

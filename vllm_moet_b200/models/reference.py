@@ -305,15 +305,20 @@ def decoder_layer(cfg, lw, x, positions, cs, cache=None, li=0):
 
 
 def forward(mw: ModelWeights, tokens: torch.Tensor, positions: torch.Tensor, cs: torch.Tensor,
-            cache: Optional[RefKV] = None):
+            cache: Optional[RefKV] = None, aux: Optional[dict] = None):
     """-> (logits [T, V] f32, the hidden state the MTP module reads: the final normed
-    hidden [T, H] f32, or with hyper-connections the streams before the head [T, n H])."""
+    hidden [T, H] f32, or with hyper-connections the streams before the head [T, n H]).
+    `aux` {layer index: None}: filled with the residual after each listed layer [T, H]
+    (hyper-connections: the mean of the streams) -- the aux hidden states a DSpark
+    drafter reads."""
     cfg = mw.cfg
     x = mw.embed[tokens].float()
     if cfg.hc_mult > 1:
         x = x[:, None, :].expand(-1, cfg.hc_mult, -1)
     for li, lw in enumerate(mw.layers):
         x = decoder_layer(cfg, lw, x, positions, cs, cache, li)
+        if aux is not None and li in aux:
+            aux[li] = x.mean(1) if x.dim() == 3 else x
     if cfg.hc_mult > 1:
         h = rms_norm(hc_head(cfg, mw.extra["hc_head"], x), mw.final_norm, cfg.rms_eps)
         return _gather_vocab(h @ mw.lm_head.dequant().t()), x.reshape(x.shape[0], -1)
