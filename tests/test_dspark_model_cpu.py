@@ -78,3 +78,19 @@ def test_engine_with_the_dspark_model(hc):
     out = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
     assert out == [ref.greedy_generate(llm.mw, p, 10) for p in prompts]
     assert llm.stats["steps"] > 0
+
+
+def test_dflash_is_the_context_drafter_without_markov_heads():
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=0, max_model_len=256, speculative_method="dflash",
+              dspark={"block": 3})
+    d = llm.runner.dspark["drafter"]
+    assert d.markov is False and llm.runner.dspark["tau"] == 0.0
+    p = [5, 6, 7, 8]
+    assert llm.generate([p], SamplingParams(max_tokens=9, ignore_eos=True))[0].outputs[0].token_ids == \
+        ref.greedy_generate(llm.mw, p, 9)
+    c = d.new_context()
+    aux = d.aux_request()
+    ref.forward(llm.mw, torch.tensor(p), torch.arange(4), d.cs, ref.RefKV(len(llm.mw.layers)), aux=aux)
+    d.extend(c, aux, 0, 4)
+    dr, base, surv = d.propose_one(c, 9, 4)
+    assert dr.tolist() == base.argmax(-1).tolist() and bool((surv == 1).all())

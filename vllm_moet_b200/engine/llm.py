@@ -80,10 +80,15 @@ class LLM:
             raise NotImplementedError("SP prefill / DCP decode / DP+EP run on the CPU engine; the GPU runner has "
                                       "none of them yet")
         self._ep_group = ep_group
-        if speculative_method not in ("mtp", "dspark"):
-            raise ValueError(f"speculative_method {speculative_method!r}: mtp | dspark")
+        if speculative_method not in ("mtp", "dspark", "dflash"):
+            raise ValueError(f"speculative_method {speculative_method!r}: mtp | dspark | dflash")
+        if speculative_method == "dflash":
+            # DFlash: the same parallel context drafter without the Markov and confidence
+            # heads; every block is verified whole
+            dspark = dict(dspark or {}, model="context", markov=False, tau=0.0, budget_frac=1.0)
+            speculative_method = "dspark"
         if speculative_method == "dspark" and self.device.type == "cuda":
-            raise NotImplementedError("DSpark block drafting runs on the CPU engine; the GPU runner drafts with MTP")
+            raise NotImplementedError("DSpark / DFlash block drafting runs on the CPU engine; the GPU runner drafts with MTP")
         if cfg.hc_mult > 1 and self.device.type == "cuda":
             raise NotImplementedError("hyper-connections (hc_mult > 1) run on the CPU engine; the GPU layer kernels "
                                       "keep one residual stream")

@@ -58,7 +58,7 @@ class TorchRunner:
                 from ..models.dspark_model import DSparkModelDrafter, random_dspark_weights
                 dw = random_dspark_weights(mw, num_layers=dspark.get("layers", 2), window=dspark.get("window", 128),
                                            seed=dspark.get("seed", 0))
-                self.dspark["drafter"] = DSparkModelDrafter(mw, dw, block, self.cs)
+                self.dspark["drafter"] = DSparkModelDrafter(mw, dw, block, self.cs, markov=dspark.get("markov", True))
             if dspark.get("cost_table") is not None:
                 pol.set_cost_table(*dspark["cost_table"])
             elif dspark.get("profile"):

@@ -151,8 +151,9 @@ class DSparkModelDrafter:
     """The drafter the engine calls: `extend` the context with verified positions'
     aux hidden states, `propose` a block per sequence."""
 
-    def __init__(self, mw: ModelWeights, dw: DSparkWeights, block: int, cs: torch.Tensor):
-        self.mw, self.dw, self.block, self.cs = mw, dw, block, cs
+    def __init__(self, mw: ModelWeights, dw: DSparkWeights, block: int, cs: torch.Tensor, markov: bool = True):
+        """markov=False: DFlash -- the block's base logits alone, survival 1 everywhere."""
+        self.mw, self.dw, self.block, self.cs, self.markov = mw, dw, block, cs, markov
         self.cfg = mw.cfg
 
     def aux_request(self) -> Dict[int, None]:
@@ -195,6 +196,8 @@ class DSparkModelDrafter:
             x = ref.hc_head(cfg, dw.hc_head, x)
         h = ref.rms_norm(x, dw.norm, cfg.rms_eps)
         base = h @ mw.lm_head.dequant().t()
+        if not self.markov:
+            return base.argmax(-1).cpu(), base, torch.ones(L, device=base.device)
         prev, drafts, conf = pending, [], []
         for j in range(L):                            # the sequential Markov walk
             e = dw.markov_w1[prev]
