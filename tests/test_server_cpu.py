@@ -196,7 +196,12 @@ def test_cli_flags_map_to_engine_arguments():
                        "min_p": 0.05, "logit_bias": {"42": -100}})
     assert (sp.presence_penalty, sp.frequency_penalty, sp.repetition_penalty, sp.min_p) == (0.5, 0.25, 1.1, 0.05)
     assert sp.logit_bias == {42: -100.0} and sp.processes_logits
-    for bad in (["--speculative-config", '{"method": "eagle"}'], ["--pipeline-parallel-size", "2"],
+    kw = llm_kwargs(build_parser().parse_args(["--speculative-config",
+                                               '{"method": "eagle3", "num_speculative_tokens": 3}']))
+    assert kw["speculative_method"] == "eagle3" and kw["num_speculative_tokens"] == 3
+    kw = llm_kwargs(build_parser().parse_args(["--speculative-config", '{"method": "dspark", "num_speculative_tokens": 4}']))
+    assert kw["speculative_method"] == "dspark" and kw["dspark"] == {"block": 4}
+    for bad in (["--speculative-config", '{"method": "ngram"}'], ["--pipeline-parallel-size", "2"],
                 ["--decode-context-parallel-size", "2"]):
         with pytest.raises(SystemExit):
             llm_kwargs(build_parser().parse_args(bad))

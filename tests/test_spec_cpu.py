@@ -2,6 +2,7 @@
 DSpark block drafter, and the greedy / stochastic rejection samplers."""
 import math
 
+import pytest
 import torch
 
 from vllm_moet_b200 import SamplingParams
@@ -236,3 +237,29 @@ def test_engine_penalties_match_token_by_token_decode():
     assert got != llm.generate([prompt], SamplingParams(max_tokens=16, ignore_eos=True))[0].outputs[0].token_ids
     forced = llm.generate([prompt], SamplingParams(max_tokens=6, ignore_eos=True, logit_bias={42: 1e4}))
     assert forced[0].outputs[0].token_ids == [42] * 6
+
+
+def test_eagle3_drafts_from_aux_hidden_states():
+    """EAGLE-3 on the CPU engine: the target returns its concatenated aux states (low /
+    middle / high layer), the draft layer chains on its own hidden state, and verification
+    keeps the output equal to the target's greedy sequence, with and without prefix
+    caching and chunked prefill."""
+    from vllm_moet_b200.models import reference
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=3, max_model_len=256, speculative_method="eagle3",
+              num_layers=3, enable_prefix_caching=True, prefix_block_size=4, enable_chunked_prefill=True,
+              max_num_batched_tokens=6)
+    ew = llm.mw.extra["eagle3"]
+    assert ew.target_layers == (0, 1, 2) and llm.mw.mtp is None and llm.k == 3
+    cs = reference.rope_cos_sin(llm.cfg, 64)
+    t = torch.tensor([5, 6, 7, 8])
+    _, hid = reference.forward(llm.mw, t, torch.arange(4), cs)
+    assert hid.shape == (4, 3 * llm.cfg.hidden)
+    lg, h = reference.mtp_forward(llm.mw, hid, torch.tensor([6, 7, 8, 9]), torch.arange(4), cs)
+    assert lg.shape == (4, llm.cfg.vocab) and h.shape == (4, llm.cfg.hidden)
+    lg2, _ = reference.mtp_forward(llm.mw, h[-1:], torch.tensor([3]), torch.tensor([4]), cs)   # chained step
+    assert lg2.shape == (1, llm.cfg.vocab)
+    prompts = [[5, 6, 7, 8, 9, 10, 11], [5, 6, 7, 8, 20]]
+    out = [o.outputs[0].token_ids for o in llm.generate(prompts, SamplingParams(max_tokens=10, ignore_eos=True))]
+    assert out == [reference.greedy_generate(llm.mw, p, 10) for p in prompts]
+    with pytest.raises(NotImplementedError):
+        LLM("tiny-moe", device="cuda", speculative_method="eagle3")

@@ -80,8 +80,11 @@ class LLM:
             raise NotImplementedError("SP prefill / DCP decode / DP+EP run on the CPU engine; the GPU runner has "
                                       "none of them yet")
         self._ep_group = ep_group
-        if speculative_method not in ("mtp", "dspark", "dflash"):
-            raise ValueError(f"speculative_method {speculative_method!r}: mtp | dspark | dflash")
+        if speculative_method not in ("mtp", "dspark", "dflash", "eagle3"):
+            raise ValueError(f"speculative_method {speculative_method!r}: mtp | dspark | dflash | eagle3")
+        if speculative_method == "eagle3" and (self.device.type == "cuda" or pipeline_parallel_size > 1):
+            raise NotImplementedError("EAGLE-3 drafting runs on the CPU engine (one pipeline stage); the GPU runner "
+                                      "drafts with MTP")
         if speculative_method == "dflash":
             # DFlash: the same parallel context drafter without the Markov and confidence
             # heads; every block is verified whole
@@ -147,7 +150,13 @@ class LLM:
             expert_source=self.expert_source)
         if self.expert_source is not None:
             self.expert_source.flush()
-        if pipeline_parallel_size > 1:
+        if speculative_method == "eagle3" and num_speculative_tokens > 0:
+            from ..models.eagle3_model import attach_eagle3, random_eagle3_weights
+            attach_eagle3(self.mw, random_eagle3_weights(self.mw, seed=seed))
+            self.mw.mtp = None                     # the EAGLE-3 module drafts instead of the MTP module
+        if speculative_method == "eagle3":
+            self._has_mtp = num_speculative_tokens > 0
+        elif pipeline_parallel_size > 1:
             # MTP presence is a property of the model, known on every stage
             self._has_mtp = num_speculative_tokens > 0 and cfg.num_mtp_layers > 0
         else:

@@ -18,7 +18,7 @@ class TorchRunner:
                  dcp_group=None, dcp_interleave: int = 1, ep_group=None, dspark: Optional[dict] = None,
                  prefix_block: int = 0, prefix_entries: int = 64):
         self.mw = mw
-        self.k = k if mw.mtp is not None and dspark is None else 0
+        self.k = k if (mw.mtp is not None or mw.extra.get("eagle3") is not None) and dspark is None else 0
         self.dspark = None              # DSpark block drafting instead of MTP: {drafter, tau, budget_frac}
         if dspark is not None:
             from ..spec.dspark import DSparkDrafter

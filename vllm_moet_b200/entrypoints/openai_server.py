@@ -536,21 +536,26 @@ def build_parser():
 def llm_kwargs(args, world: int = 1, rank: int = 0, group=None) -> dict:
     """Server flags -> LLM keyword arguments (refusing what the GPU server path does not serve)."""
     k = args.num_speculative_tokens
+    method = "mtp"
     if args.speculative_config:
         spec = json.loads(args.speculative_config)
         method = spec.get("method", "mtp")
-        if method not in ("mtp", "deepseek_mtp", "deepseek_v4_mtp"):
-            raise SystemExit(f"speculative method {method!r}: this engine drafts with the model's MTP module")
+        if method in ("mtp", "deepseek_mtp", "deepseek_v4_mtp"):
+            method = "mtp"
+        elif method not in ("eagle3", "dspark", "dflash"):       # these three: CPU engine
+            raise SystemExit(f"speculative method {method!r}: mtp | eagle3 | dspark | dflash")
         k = int(spec.get("num_speculative_tokens", k))
     if args.pipeline_parallel_size != 1:
         raise SystemExit("--pipeline-parallel-size: the server runs TP ranks; use the LLM API for pipeline stages")
     if args.decode_context_parallel_size != 1:
         raise SystemExit("--decode-context-parallel-size: DCP runs on the CPU engine only so far")
     kv = "nvfp4" if args.kv_cache_dtype == "nvfp4" else "bf16"
-    return dict(device=args.device, num_speculative_tokens=k, max_model_len=args.max_model_len,
+    return dict(device=args.device, num_speculative_tokens=0 if method in ("dspark", "dflash") else k,
+                max_model_len=args.max_model_len,
                 max_num_seqs=args.max_num_seqs, num_layers=args.num_layers, kv_cache_dtype=kv,
                 tensor_parallel_size=world, tp_group=group, tp_rank=rank,
-                expert_parallel=bool(args.enable_expert_parallel),
+                expert_parallel=bool(args.enable_expert_parallel), speculative_method=method,
+                **({"dspark": {"block": k}} if method in ("dspark", "dflash") else {}),
                 enable_prefix_caching=bool(getattr(args, "enable_prefix_caching", False)),
                 prefix_block_size=int(getattr(args, "block_size", 16)),
                 enable_chunked_prefill=bool(getattr(args, "enable_chunked_prefill", False)),

@@ -312,6 +312,11 @@ def forward(mw: ModelWeights, tokens: torch.Tensor, positions: torch.Tensor, cs:
     (hyper-connections: the mean of the streams) -- the aux hidden states a DSpark
     drafter reads."""
     cfg = mw.cfg
+    eagle = mw.extra.get("eagle3")
+    if eagle is not None:                       # EAGLE-3 drafts from the concatenated aux states
+        aux = {} if aux is None else aux
+        for li in eagle.target_layers:
+            aux.setdefault(li, None)
     x = mw.embed[tokens].float()
     if cfg.hc_mult > 1:
         x = x[:, None, :].expand(-1, cfg.hc_mult, -1)
@@ -319,6 +324,14 @@ def forward(mw: ModelWeights, tokens: torch.Tensor, positions: torch.Tensor, cs:
         x = decoder_layer(cfg, lw, x, positions, cs, cache, li)
         if aux is not None and li in aux:
             aux[li] = x.mean(1) if x.dim() == 3 else x
+    if eagle is not None:
+        logits, _ = _head(mw, x)
+        return logits, torch.cat([aux[li] for li in eagle.target_layers], -1)
+    return _head(mw, x)
+
+
+def _head(mw: ModelWeights, x: torch.Tensor):
+    cfg = mw.cfg
     if cfg.hc_mult > 1:
         h = rms_norm(hc_head(cfg, mw.extra["hc_head"], x), mw.final_norm, cfg.rms_eps)
         return _gather_vocab(h @ mw.lm_head.dequant().t()), x.reshape(x.shape[0], -1)
@@ -330,6 +343,9 @@ def mtp_forward(mw: ModelWeights, hidden: torch.Tensor, next_tokens: torch.Tenso
                 cs: torch.Tensor, cache: Optional[RefKV] = None):
     """MTP module: (h_i, token_{i+1}) at position i -> logits for token_{i+2}; returns (logits, hidden)."""
     cfg, m = mw.cfg, mw.mtp
+    if mw.extra.get("eagle3") is not None:
+        from .eagle3_model import eagle3_forward
+        return eagle3_forward(mw, hidden, next_tokens, positions, cs, cache)
     if cfg.hc_mult > 1:
         return _mtp_forward_hc(mw, hidden, next_tokens, positions, cs, cache)
     e = rms_norm(mw.embed[next_tokens].float(), m.enorm, cfg.rms_eps)
