@@ -758,7 +758,7 @@ class NativeRunner:
         outputs of argmax + mtp_accept), in graph-safe tensor ops."""
         from ..spec.device_sampler import sample_verify
         B, kp1 = st.B, self.k + 1
-        logits = self._full_vocab(logits).view(B, kp1, -1)
+        logits = self._full_vocab(logits).reshape(B, kp1, -1)
         if st.proc is not None:               # penalties / logit bias, verify row j after drafts[:j]
             logits = self._process(st, logits, st.tokens[:, 1:], None)
         n, tok = sample_verify(logits, st.tokens[:, 1:], st.temperature, st.top_k, st.top_p,
@@ -782,7 +782,7 @@ class NativeRunner:
         dev = logits.device
         B = len(seq_rows)
         r = torch.tensor(seq_rows, dtype=torch.long, device=dev)
-        x = self._full_vocab(logits).view(B, 1, -1)
+        x = self._full_vocab(logits).reshape(B, 1, -1)
         none = torch.zeros(B, 0, dtype=torch.int32, device=dev)
         if state.proc is not None:
             x = self._process(state, x, none, r)
