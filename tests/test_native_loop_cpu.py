@@ -42,6 +42,10 @@ class FakeRunner:
         self.k, self.graphs, self.steps = k, {}, 0
         self.ws_prefill = self
         self.logits = {}
+        self.starts_log, self.copies = [], []
+
+    def copy_block(self, src, dst):
+        self.copies.append((src, dst))
 
     def _drafts(self, t, p):
         d = []
@@ -52,7 +56,8 @@ class FakeRunner:
             d[-1] = (d[-1] + 1) % V
         return d
 
-    def prefill(self, prompts, bts, rows, st, sample=False):
+    def prefill(self, prompts, bts, rows, st, sample=False, starts=None):
+        self.starts_log.append(list(starts) if starts is not None else [0] * len(prompts))
         firsts = []
         for pr, r in zip(prompts, rows):
             t0 = f(pr[-1], len(pr) - 1)
@@ -147,14 +152,14 @@ def engine(monkeypatch):
     monkeypatch.setattr(torch, "zeros", zeros_no_pin)
     monkeypatch.setattr(torch.cuda, "current_stream", lambda *a, **k: _Stream())
 
-    def make(max_num_seqs=4, k=2):
+    def make(max_num_seqs=4, k=2, prefix_caching=False):
         llm = object.__new__(LLM)
         cfg = tiny_config()
         llm.cfg, llm.k, llm.device = cfg, k, torch.device("cpu")
         llm.ecfg = EngineConfig(model=cfg, moet=MoetConfig(), max_num_seqs=max_num_seqs, max_model_len=512,
                                 num_speculative_tokens=k, cuda_graphs=False)
         llm.max_blocks = -(-(512 + k + 2) // 64)
-        llm.blocks = BlockManager(max_num_seqs * llm.max_blocks + 1)
+        llm.blocks = BlockManager(max_num_seqs * llm.max_blocks + 1, prefix_caching=prefix_caching)
         llm.tokenizer = ByteTokenizer(V)
         llm._states, llm._DecodeState, llm._ids = {}, DecodeState, itertools.count()
         llm.cache = llm.delta = llm.gate = llm.routing = llm.timers = None
@@ -311,3 +316,20 @@ def test_penalties_in_the_gpu_loop(engine):
     pen = SamplingParams(max_tokens=6, ignore_eos=True, logit_bias={77: 11.0}, presence_penalty=2.0)
     got = llm.generate([[9, 10]], pen)[0].outputs[0].token_ids
     assert got[0] == 77 and 77 not in got[1:]
+
+
+def test_prefix_sharing_in_the_gpu_loop(engine):
+    """GPU prefix caching, host side: a second request sharing 2 full blocks (128 tokens)
+    maps the first block, copies the second (copy-on-write) and prefills from position
+    127; outputs are the model's chain and every block is accounted for at the end."""
+    llm = engine(prefix_caching=True)
+    prefix = [(7 * i) % 1000 + 3 for i in range(128)]
+    a, b = prefix + [5, 6, 7], prefix + [9]
+    sp = SamplingParams(max_tokens=6, ignore_eos=True)
+    assert llm.generate([a], sp)[0].outputs[0].token_ids == chain(a, 6)
+    assert llm.runner.starts_log[-1] == [0] and not llm.runner.copies
+    assert llm.generate([b], sp)[0].outputs[0].token_ids == chain(b, 6)
+    assert llm.runner.starts_log[-1] == [127] and len(llm.runner.copies) == 1
+    bm = llm.blocks
+    assert bm.stats["hit_blocks"] == 2 and not bm.owned
+    bm.check_invariants()

@@ -185,3 +185,25 @@ def test_logit_bias_and_penalties_on_the_gpu(llm):
     once = SamplingParams(max_tokens=6, ignore_eos=True, logit_bias={42: 1e3}, presence_penalty=2.0,
                           frequency_penalty=2.0)
     assert llm.generate([p], once)[0].outputs[0].token_ids == [42] * 6
+
+
+def test_prefix_cached_prefill_matches_full_prefill():
+    """GPU prefix caching: the second prompt's shared 128-token prefix is read from the
+    first prompt's blocks (one copied, position 127 recomputed) and only the rest runs
+    through the absorbed-attention ("cached") prefill; its last logits match a full
+    prefill of the same prompt."""
+    pc = LLM(small_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=1024, max_num_seqs=4,
+             enable_prefix_caching=True)
+    prefix = _prompt(128, 21)
+    a, b = prefix + _prompt(20, 22), prefix + _prompt(30, 23)
+    sp = SamplingParams(max_tokens=4, ignore_eos=True)
+    pc.generate([a], sp)
+    got = pc.generate([b], sp)[0].outputs[0].token_ids
+    lg_cached = pc.runner.ws_prefill.bufs[("main.logits", torch.float32)][: pc.cfg.vocab].clone()
+    assert pc.blocks.stats["hit_blocks"] == 2 and len(got) == 4
+    full = LLM(small_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=1024, max_num_seqs=4)
+    want = full.generate([b], sp)[0].outputs[0].token_ids
+    lg_full = full.runner.ws_prefill.bufs[("main.logits", torch.float32)][: full.cfg.vocab].clone()
+    rel = float((lg_cached - lg_full).norm() / lg_full.norm())
+    assert rel < 0.05, rel
+    assert got[0] == want[0] or float(lg_full[got[0]]) >= float(lg_full.max()) - 0.3

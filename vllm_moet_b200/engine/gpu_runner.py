@@ -71,7 +71,8 @@ class StepCtx:
     seq: torch.Tensor            # [T] int32 (row into block_table)
     slot: torch.Tensor           # [T] int64
     block_table: torch.Tensor    # [S, max_blocks] int32
-    mode: str                    # "decode" | "prefill"
+    mode: str                    # "decode" | "prefill" | "cached" (prefill compute, attention over the
+                                 # paged cache: a prompt whose leading positions are already cached)
     cu_seqlens: Optional[torch.Tensor] = None
     max_len: int = 0
     mb: int = 8                  # rows per expert pair
@@ -361,7 +362,8 @@ class NativeRunner:
         else:
             self._norm_in(x, lw.attn_norm, None, hq, hs)
             self._gemv(hq, hs, lw.qkv_a, qkva)
-        if ctx.mode == "decode":
+        absorbed = ctx.mode in ("decode", "cached")     # attention reads the paged latent cache
+        if absorbed:
             with self._fork():     # latent KV path (norm, rope, cache write) beside the query path
                 C.kv_prep(qkva[:, ql:], lat, rope, lw.kv_a_norm, cfg.rms_eps, ctx.pos, self.cos_sin, ctx.slot,
                           self.kv_mode, cache, None, None, None, None, self.status)
@@ -372,7 +374,7 @@ class NativeRunner:
             C.rmsnorm_quant(qkva[:, :ql], None, None, lw.q_a_norm, cfg.rms_eps, None, qaq, qas, None, None, 0)
             self._gemv(qaq, qas, lw.q_b, qb)
         sel = self._indexer(lw, hq, hs, qaq, qas, ctx, li) if lw.idx_wq is not None else None
-        if ctx.mode == "decode":
+        if absorbed:
             qnq = self.ws.get("qn.q", (T, Hh, nope), torch.uint8)
             qns = self.ws.get("qn.s", (T, Hh, nope // 64), torch.uint8)
             qcat = self.ws.get("qcat", (T, Hh, lat + rope), torch.bfloat16)
@@ -409,7 +411,7 @@ class NativeRunner:
         ki = self.ws.get("idx.k", (T, Di), torch.bfloat16)
         self._gemv(hq, hs, lw.idx_wk, ki)
         C.idx_k_write(ki, ctx.slot, self.idx_kv[li], self.status)
-        if ctx.mode != "decode":
+        if ctx.mode == "prefill":
             return None
         qi = self.ws.get("idx.q", (T, Hi * Di), torch.bfloat16)
         self._gemv(qaq, qas, lw.idx_wq, qi)
@@ -462,7 +464,7 @@ class NativeRunner:
         ep = ex.n_local is not None
         E_loc = ex.n_local if ep else E
         e_lo = ex.e_lo if ep else -1
-        use_tc = ctx.mode == "prefill" and H % 128 == 0 and I % 128 == 0 and (2 * I) % 128 == 0
+        use_tc = ctx.mode in ("prefill", "cached") and H % 128 == 0 and I % 128 == 0 and (2 * I) % 128 == 0
         topp = self.ecfg.moet.topp
         if T <= 64 and not use_tc and H % 1024 == 0 and topp <= 0:
             # decode: logits + top-k + pair list in one launch
@@ -595,7 +597,7 @@ class NativeRunner:
         self._fused = self.ar is not None and ctx.mode == "decode" and self.ar.fits(ctx.T, H)
         self._decode = ctx.mode == "decode"
         x2 = self.ws.get("x_mid", (ctx.T, H), torch.bfloat16)
-        timed = self.timers is not None and ctx.mode == "prefill"
+        timed = self.timers is not None and ctx.mode in ("prefill", "cached")
         with self.timers.span("prefill.attention") if timed else contextlib.nullcontext():
             self._attention(lw, x, ctx, cache, li, x2)
         self._check(f"attention[{li}] ({ctx.mode})", x2)
@@ -653,14 +655,21 @@ class NativeRunner:
 
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
-    def prefill(self, prompts: list, block_tables: list, seq_rows: list, state, sample: bool = False):
+    def copy_block(self, src: int, dst: int):
+        """Copy one KV block (every layer's latent cache, the MTP layer's and the indexer's):
+        the copy-on-write step of prefix sharing."""
+        for t in list(self.kv) + list(getattr(self, "idx_kv", None) or []):
+            t[dst].copy_(t[src])
+
+    def prefill(self, prompts: list, block_tables: list, seq_rows: list, state, sample: bool = False,
+                starts: Optional[list] = None):
         """Prefill whole prompts (one chunk each); fills main + MTP caches and the
         decode state rows `seq_rows` (tokens, positions, drafts).  Returns the
         first generated token of each prompt.  `sample`: the first tokens are drawn with
         the rows' sampling parameters (already set in `state`)."""
         self.ws = self.ws_prefill
         try:
-            out = self._prefill(prompts, block_tables, seq_rows, state, sample)
+            out = self._prefill(prompts, block_tables, seq_rows, state, sample, starts)
         finally:
             self.ws = self.ws_prefill
         self.check_status("prefill")
@@ -673,22 +682,26 @@ class NativeRunner:
             names = {1: "index out of range", 2: "bounded wait timed out", 3: "bad size", 4: "non-finite logits"}
             raise RuntimeError(f"device status {code} ({names.get(code, '?')}) during {where}")
 
-    def _prefill(self, prompts, block_tables, seq_rows, state, sample=False):
+    def _prefill(self, prompts, block_tables, seq_rows, state, sample=False, starts=None):
+        """`starts[i]` > 0: positions [0, starts[i]) of prompt i are already in its blocks
+        (a shared prefix); only the rest runs, in "cached" mode."""
         dev, C = self.dev, self.C
-        lens = [len(p) for p in prompts]
+        starts = list(starts) if starts is not None else [0] * len(prompts)
+        full = [len(p) for p in prompts]
+        lens = [n - s0 for n, s0 in zip(full, starts)]                  # rows computed per prompt
         T = sum(lens)
-        toks = torch.tensor([t for p in prompts for t in p], dtype=torch.int32, device=dev)
-        pos = torch.cat([torch.arange(n, dtype=torch.int32) for n in lens]).to(dev)
+        toks = torch.tensor([t for p, s0 in zip(prompts, starts) for t in p[s0:]], dtype=torch.int32, device=dev)
+        pos = torch.cat([torch.arange(s0, n, dtype=torch.int32) for s0, n in zip(starts, full)]).to(dev)
         seq = torch.cat([torch.full((n,), i, dtype=torch.int32) for i, n in enumerate(lens)]).to(dev)
         bt = torch.tensor(block_tables, dtype=torch.int32, device=dev)
         slot = (bt[seq.long(), (pos // KV_BLOCK).long()].long() * KV_BLOCK + (pos % KV_BLOCK).long())
         cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=dev)
-        ctx = StepCtx(T=T, pos=pos, seq=seq, slot=slot, block_table=bt, mode="prefill", cu_seqlens=cu,
-                      max_len=max(lens), mb=32)
+        ctx = StepCtx(T=T, pos=pos, seq=seq, slot=slot, block_table=bt,
+                      mode="cached" if any(starts) else "prefill", cu_seqlens=cu, max_len=max(lens), mb=32)
         x = self._main(toks, ctx)
         B = len(prompts)
         if not self.last_stage:     # the last stage computes the first tokens and drafts, then broadcasts them
-            cur = torch.tensor(lens, dtype=torch.int32, device=dev)
+            cur = torch.tensor(full, dtype=torch.int32, device=dev)
             state.set_rows(seq_rows, torch.zeros(B, dtype=torch.int32, device=dev), cur,
                            torch.zeros(B, max(self.k, 1), dtype=torch.int32, device=dev)[:, :self.k] if self.k else None)
             self._pp_broadcast_state(state)
@@ -698,11 +711,11 @@ class NativeRunner:
         hid_last, logits = self._final(xl, None, "main")
         tgt = self.ws.get("pf.tgt", (len(prompts),), torch.int32)
         if sample:
-            tgt.copy_(self._sample_first(state, seq_rows, logits, lens))
+            tgt.copy_(self._sample_first(state, seq_rows, logits, full))
         else:
             self._argmax(logits, tgt)
         if self.k == 0:
-            state.set_rows(seq_rows, tgt, torch.tensor(lens, dtype=torch.int32, device=dev), None)
+            state.set_rows(seq_rows, tgt, torch.tensor(full, dtype=torch.int32, device=dev), None)
             self._pp_broadcast_state(state)
             return tgt
         # full hidden for the MTP pass: final norm over all rows
@@ -717,7 +730,7 @@ class NativeRunner:
         self._argmax(ml, d1)
         drafts[:, 0] = d1
         h_prev = mh.clone()
-        cur_pos = torch.tensor(lens, dtype=torch.int32, device=dev)  # position of the first generated token
+        cur_pos = torch.tensor(full, dtype=torch.int32, device=dev)  # position of the first generated token
         prev_tok = d1
         for j in range(1, self.k):
             p2 = cur_pos + (j - 1)

@@ -110,8 +110,6 @@ class LLM:
             self._chunk_budget = int(max_num_batched_tokens or 2048)
             if self._chunk_budget < 1:
                 raise ValueError("max_num_batched_tokens must be >= 1")
-        if enable_prefix_caching and self.device.type == "cuda":
-            raise NotImplementedError("prefix caching runs on the CPU engine; GPU prefill starts at position 0")
         if enable_prefix_caching and (sp_group is not None or dcp_group is not None):
             raise ValueError("prefix caching keeps whole per-sequence caches: not with SP prefill / DCP decode")
         if self.device.type == "cuda" and cfg.expert_scale != "ue8m0":
@@ -168,7 +166,7 @@ class LLM:
         if self.device.type == "cuda":
             from .gpu_runner import DecodeState, NativeRunner
             nb = num_gpu_blocks or (max_num_seqs * self.max_blocks + 1)
-            self.blocks = BlockManager(nb)
+            self.blocks = BlockManager(nb, prefix_caching=enable_prefix_caching)
             self.runner = NativeRunner(self.mw, self.ecfg, nb, self.device)
             if tp_group is not None:
                 self.runner.set_tp_group(tp_group)
@@ -676,11 +674,25 @@ class LLM:
                 bt_host, B = bt_new, B_new
             free = [i for i, r in enumerate(rows) if r is None]
             adm = []
-            while waiting and free and self.blocks.can_allocate(len(waiting[0].prompt) + waiting[0].params.max_tokens + kp1 + 1):
+            pc = getattr(self.blocks, "prefix_caching", False)
+            starts = []
+            while waiting and free and self.blocks.can_allocate(
+                    len(waiting[0].prompt) + waiting[0].params.max_tokens + kp1 + 1, waiting[0].prompt if pc else None):
                 r = waiting.popleft()
                 r.row = free.pop(0)
                 rows[r.row] = r
-                blocks = self.blocks.allocate(r.rid, len(r.prompt) + r.params.max_tokens + kp1 + 1)
+                n_tok = len(r.prompt) + r.params.max_tokens + kp1 + 1
+                if pc:
+                    # shared prefix blocks; the block holding the position before the first new
+                    # token is copied and that position computed again (its MTP entry differs)
+                    blocks, m, cow = self.blocks.allocate_with_prefix(r.rid, n_tok, r.prompt)
+                    if cow is not None:
+                        runner.copy_block(*cow)
+                        self.blocks.copied(r.rid)
+                    starts.append(max(m - 1, 0))
+                else:
+                    blocks = self.blocks.allocate(r.rid, n_tok)
+                    starts.append(0)
                 bt_host[r.row].zero_()
                 bt_host[r.row, :len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
                 adm.append(r)
@@ -691,8 +703,11 @@ class LLM:
                 bts = [bt_host[r.row].tolist() for r in adm]
                 sample_pf = self._set_sampling(st, adm)
                 with self.timers.span("prefill") if self.timers is not None else contextlib.nullcontext():
-                    firsts = runner.prefill([r.prompt for r in adm], bts, [r.row for r in adm], st,
-                                            **({"sample": True} if sample_pf else {})).tolist()
+                    kw = dict(({"sample": True} if sample_pf else {}), **({"starts": starts} if any(starts) else {}))
+                    firsts = runner.prefill([r.prompt for r in adm], bts, [r.row for r in adm], st, **kw).tolist()
+                if pc:
+                    for r in adm:
+                        self.blocks.register(r.rid, r.prompt)
                 now = time.perf_counter()
                 want_lp = any(r.params.logprobs is not None for r in adm)
                 pl = runner.ws_prefill.get("main.logits", (len(adm), self.cfg.vocab), torch.float32) if want_lp \
