@@ -305,5 +305,3 @@ def test_chunked_prefill_interleaves_with_decode():
         assert all(d - b <= 8 for _, b, d, _ in log)
         assert sum(1 for c in log if c[3] == 1) >= 5             # chunks that ran beside a decoding row
         assert llm.stats["prefill_chunks"] == len(llm._chunk_log)
-    with pytest.raises(NotImplementedError):
-        LLM("tiny-moe", device="cuda", enable_chunked_prefill=True)

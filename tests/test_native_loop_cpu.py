@@ -42,10 +42,13 @@ class FakeRunner:
         self.k, self.graphs, self.steps = k, {}, 0
         self.ws_prefill = self
         self.logits = {}
-        self.starts_log, self.copies = [], []
+        self.starts_log, self.copies, self.chunks = [], [], []
 
     def copy_block(self, src, dst):
         self.copies.append((src, dst))
+
+    def prefill_chunk(self, prompt, bt, start, end):
+        self.chunks.append((start, end))
 
     def _drafts(self, t, p):
         d = []
@@ -152,7 +155,7 @@ def engine(monkeypatch):
     monkeypatch.setattr(torch, "zeros", zeros_no_pin)
     monkeypatch.setattr(torch.cuda, "current_stream", lambda *a, **k: _Stream())
 
-    def make(max_num_seqs=4, k=2, prefix_caching=False):
+    def make(max_num_seqs=4, k=2, prefix_caching=False, chunk=None):
         llm = object.__new__(LLM)
         cfg = tiny_config()
         llm.cfg, llm.k, llm.device = cfg, k, torch.device("cpu")
@@ -165,6 +168,7 @@ def engine(monkeypatch):
         llm.cache = llm.delta = llm.gate = llm.routing = llm.timers = None
         llm._tp_group = llm._pp_group = llm._ep_group = None
         llm._decode_steps, llm.stats = 0, {}
+        llm._chunk_budget = chunk
         llm.runner = FakeRunner(k)
         llm._run_torch = types.MethodType(LLM._run_native, llm)    # generate() dispatches by device type
         return llm
@@ -333,3 +337,18 @@ def test_prefix_sharing_in_the_gpu_loop(engine):
     bm = llm.blocks
     assert bm.stats["hit_blocks"] == 2 and not bm.owned
     bm.check_invariants()
+
+
+def test_chunked_prefill_in_the_gpu_loop(engine):
+    """GPU chunked prefill, host side: a 50-token prompt is prefilled 5 tokens a step
+    (budget 8 minus the decoding row's k + 1 = 3) beside a decoding request; the last
+    chunk is a prefill from its start position; both outputs are the model's chain."""
+    llm = engine(chunk=8)
+    short, long_ = [5, 6, 7], list(range(10, 60))
+    out = llm.generate([short, long_], SamplingParams(max_tokens=30, ignore_eos=True))
+    assert out[0].outputs[0].token_ids == chain(short, 30) and out[1].outputs[0].token_ids == chain(long_, 30)
+    log = [c for c in llm._chunk_log if c[0] == out[1].request_id]
+    assert log[0][1] == 0 and log[-1][2] == 50 and all(e - s <= 8 for _, s, e, _ in log)
+    assert sum(1 for c in log if c[3] == 1) >= 5                   # chunks beside the decoding row
+    assert llm.runner.chunks == [(s, e) for _, s, e, _ in log[:-1]]
+    assert llm.runner.starts_log[-1] == [log[-1][1]]

@@ -207,3 +207,20 @@ def test_prefix_cached_prefill_matches_full_prefill():
     rel = float((lg_cached - lg_full).norm() / lg_full.norm())
     assert rel < 0.05, rel
     assert got[0] == want[0] or float(lg_full[got[0]]) >= float(lg_full.max()) - 0.3
+
+
+def test_chunked_prefill_matches_full_prefill():
+    """GPU chunked prefill: a 150-token prompt prefilled 48 tokens a step (first chunk
+    dense, then the cached mode) ends with the same last logits as one full prefill."""
+    ch = LLM(small_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=1024, max_num_seqs=4,
+             enable_chunked_prefill=True, max_num_batched_tokens=48)
+    p = _prompt(150, 31)
+    sp = SamplingParams(max_tokens=4, ignore_eos=True)
+    got = ch.generate([p], sp)[0].outputs[0].token_ids
+    lg_chunked = ch.runner.ws_prefill.bufs[("main.logits", torch.float32)][: ch.cfg.vocab].clone()
+    assert len(ch._chunk_log) == 4 and len(got) == 4
+    full = LLM(small_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=1024, max_num_seqs=4)
+    full.generate([p], sp)
+    lg_full = full.runner.ws_prefill.bufs[("main.logits", torch.float32)][: full.cfg.vocab].clone()
+    rel = float((lg_chunked - lg_full).norm() / lg_full.norm())
+    assert rel < 0.05, rel

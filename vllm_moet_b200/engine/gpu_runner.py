@@ -655,6 +655,32 @@ class NativeRunner:
 
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
+    @torch.no_grad()
+    def prefill_chunk(self, prompt: list, block_table: list, start: int, end: int):
+        """A non-final chunk of a chunked prefill: positions [start, end) of `prompt`
+        (end < len(prompt)) through the main layers and the MTP layer, caches written, no
+        head.  Every MTP row's next token is a prompt token, so nothing is recomputed
+        later; the final chunk is a `prefill` with starts=[end]."""
+        assert 0 <= start < end < len(prompt)
+        self.ws = self.ws_prefill
+        dev, T = self.dev, end - start
+        toks = torch.tensor(prompt[start:end], dtype=torch.int32, device=dev)
+        pos = torch.arange(start, end, dtype=torch.int32, device=dev)
+        seq = torch.zeros(T, dtype=torch.int32, device=dev)
+        bt = torch.tensor([block_table], dtype=torch.int32, device=dev)
+        slot = bt[0, (pos // KV_BLOCK).long()].long() * KV_BLOCK + (pos % KV_BLOCK).long()
+        cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
+        ctx = StepCtx(T=T, pos=pos, seq=seq, slot=slot, block_table=bt, mode="cached" if start else "prefill",
+                      cu_seqlens=cu, max_len=T, mb=32)
+        x = self._main(toks, ctx)
+        if self.last_stage and self.k:
+            hid_all = self.ws.get("pf.hid", (T, self.cfg.hidden), torch.bfloat16)
+            self.C.rmsnorm_quant(x, None, None, self.mw.final_norm, self.cfg.rms_eps, hid_all, None, None, None,
+                                 None, 0)
+            nxt = torch.tensor(prompt[start + 1:end + 1], dtype=torch.int32, device=dev)
+            self._mtp(hid_all, nxt, ctx, rows=torch.tensor([T - 1], device=dev))
+        self.check_status("prefill chunk")
+
     def copy_block(self, src: int, dst: int):
         """Copy one KV block (every layer's latent cache, the MTP layer's and the indexer's):
         the copy-on-write step of prefix sharing."""

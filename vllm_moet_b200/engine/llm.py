@@ -102,9 +102,6 @@ class LLM:
                                       "(both read a single-stream hidden state)")
         self._chunk_budget = None
         if enable_chunked_prefill:
-            if self.device.type == "cuda":
-                raise NotImplementedError("chunked prefill runs on the CPU engine; the GPU prefill kernels start "
-                                          "at position 0")
             if sp_group is not None or dcp_group is not None or ep_group is not None:
                 raise ValueError("chunked prefill: not with SP prefill, DCP decode or DP + EP")
             self._chunk_budget = int(max_num_batched_tokens or 2048)
@@ -655,6 +652,8 @@ class LLM:
         steps = accepted = 0
         t_decode = 0.0
         bt_host = torch.zeros(B, self.max_blocks, dtype=torch.int32)
+        prefilling = {}            # row -> (request, next prompt position, samples) of a chunked prefill
+        self._chunk_log = []
         while True:
             # serving: the batch may grow into a larger bucket, so offer room up to `cap` rows
             room = (cap if self._between is not None else B) - sum(r is not None for r in rows) - len(waiting)
@@ -700,25 +699,15 @@ class LLM:
                 raise MemoryError("KV cache too small for the next request")
             if adm:
                 st.block_table.copy_(bt_host, non_blocking=False)
-                bts = [bt_host[r.row].tolist() for r in adm]
                 sample_pf = self._set_sampling(st, adm)
-                with self.timers.span("prefill") if self.timers is not None else contextlib.nullcontext():
-                    kw = dict(({"sample": True} if sample_pf else {}), **({"starts": starts} if any(starts) else {}))
-                    firsts = runner.prefill([r.prompt for r in adm], bts, [r.row for r in adm], st, **kw).tolist()
-                if pc:
-                    for r in adm:
-                        self.blocks.register(r.rid, r.prompt)
-                now = time.perf_counter()
-                want_lp = any(r.params.logprobs is not None for r in adm)
-                pl = runner.ws_prefill.get("main.logits", (len(adm), self.cfg.vocab), torch.float32) if want_lp \
-                    else None
-                if getattr(st, "proc", None) is not None:
-                    st.count_tokens([r.row for r in adm], firsts)
-                for j, (r, f) in enumerate(zip(adm, firsts)):
-                    r.t_first = now
-                    if self._emit(r, [f], pl[j:j + 1] if pl is not None else None):
-                        self._finish_row(r, rows)
-            live = [r is not None for r in rows]
+                if self._chunk_budget is not None:
+                    for r, s0 in zip(adm, starts):
+                        prefilling[r.row] = (r, s0, sample_pf)
+                else:
+                    self._prefill_rows(adm, starts, sample_pf, st, bt_host, rows)
+            if prefilling:
+                self._gpu_chunks(prefilling, st, bt_host, rows)
+            live = [r is not None and i not in prefilling for i, r in enumerate(rows)]
             if not any(live):
                 continue
             for i, on in enumerate(live):
@@ -765,13 +754,13 @@ class LLM:
             if getattr(st, "proc", None) is not None:          # generated-token counts for the penalties
                 cr, ct = [], []
                 for i, r in enumerate(rows):
-                    if r is not None:
+                    if r is not None and i not in prefilling:
                         n_i = int(pin_acc[i]) + 1
                         cr += [i] * n_i
                         ct += pin_out[i, :n_i].tolist()
                 st.count_tokens(cr, ct)
             for i, r in enumerate(rows):
-                if r is None:
+                if r is None or i in prefilling:
                     continue
                 a = int(pin_acc[i])
                 accepted += a
@@ -779,6 +768,56 @@ class LLM:
                 if self._emit(r, pin_out[i, :a + 1].tolist(), lg):
                     self._finish_row(r, rows)
         self.stats = dict(steps=steps, accepted=accepted, decode_s=t_decode, bucket=B)
+
+    def _prefill_rows(self, adm, starts, sample_pf, st, bt_host, rows):
+        """Prefill admitted requests whose positions before `starts` are cached; emit their
+        first tokens."""
+        runner = self.runner
+        bts = [bt_host[r.row].tolist() for r in adm]
+        with self.timers.span("prefill") if self.timers is not None else contextlib.nullcontext():
+            kw = dict(({"sample": True} if sample_pf else {}), **({"starts": starts} if any(starts) else {}))
+            firsts = runner.prefill([r.prompt for r in adm], bts, [r.row for r in adm], st, **kw).tolist()
+        if getattr(self.blocks, "prefix_caching", False):
+            for r in adm:
+                self.blocks.register(r.rid, r.prompt)
+        now = time.perf_counter()
+        want_lp = any(r.params.logprobs is not None for r in adm)
+        pl = runner.ws_prefill.get("main.logits", (len(adm), self.cfg.vocab), torch.float32) if want_lp else None
+        if getattr(st, "proc", None) is not None:
+            st.count_tokens([r.row for r in adm], firsts)
+        for j, (r, f) in enumerate(zip(adm, firsts)):
+            r.t_first = now
+            if self._emit(r, [f], pl[j:j + 1] if pl is not None else None):
+                self._finish_row(r, rows)
+
+    def _gpu_chunks(self, prefilling, st, bt_host, rows):
+        """Chunked prefill on the GPU runner: the step's token budget goes to the decoding
+        rows first ((k + 1) each), the rest to prefills in arrival order.  A non-final chunk
+        runs `prefill_chunk`; the last one is a prefill from its start position."""
+        kp1 = self.k + 1
+        n_dec = sum(1 for i, r in enumerate(rows) if r is not None and i not in prefilling)
+        budget = max(self._chunk_budget - n_dec * kp1, 1)
+        finals = []
+        for row in list(prefilling):
+            r, s0, smp = prefilling[row]
+            if rows[row] is not r:                     # aborted while prefilling
+                del prefilling[row]
+                continue
+            if budget <= 0:
+                break
+            n = len(r.prompt)
+            e = min(n, s0 + budget)
+            self._chunk_log.append((r.rid, s0, e, n_dec))
+            budget -= e - s0
+            if e < n:
+                self.runner.prefill_chunk(r.prompt, bt_host[row].tolist(), s0, e)
+                prefilling[row] = (r, e, smp)
+            else:
+                finals.append((r, s0, smp))
+                del prefilling[row]
+        if finals:
+            self._prefill_rows([f[0] for f in finals], [f[1] for f in finals], any(f[2] for f in finals), st,
+                               bt_host, rows)
 
     def _decode_eager(self, st):
         if getattr(self, "_step_sample", False):
