@@ -317,3 +317,23 @@ def test_chat_stream_over_http(server):
               if ln.startswith("data: ") and ln != "data: [DONE]"]
     assert events[0]["choices"][0]["delta"]["role"] == "assistant"
     assert events[-1]["choices"][0]["finish_reason"] == "length"
+
+
+def test_echo_and_stream_usage(server):
+    url, _ = server
+    body = {"prompt": "abc", "max_tokens": 4, "ignore_eos": True, "echo": True}
+    r = requests.post(url + "/v1/completions", json=body, timeout=120).json()
+    assert r["choices"][0]["text"].startswith("abc")
+    r = requests.post(url + "/v1/completions", json=dict(body, stream=True, stream_options={"include_usage": True}),
+                      stream=True, timeout=120)
+    events = [json.loads(ln[6:]) for ln in r.iter_lines(decode_unicode=True)
+              if ln.startswith("data: ") and ln != "data: [DONE]"]
+    assert events[0]["choices"][0]["text"] == "abc"                      # echoed prompt first
+    assert events[-1]["choices"] == [] and events[-1]["usage"]["completion_tokens"] == 4
+    r = requests.post(url + "/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}],
+                                                          "max_tokens": 3, "ignore_eos": True, "stream": True,
+                                                          "stream_options": {"include_usage": True}},
+                      stream=True, timeout=120)
+    events = [json.loads(ln[6:]) for ln in r.iter_lines(decode_unicode=True)
+              if ln.startswith("data: ") and ln != "data: [DONE]"]
+    assert events[-1]["usage"]["completion_tokens"] == 3 and events[-1]["usage"]["prompt_tokens"] > 0

@@ -374,8 +374,21 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
                 for j in range(params.n)]
 
     def _servable(params):
-        if params.temperature > 0 and worker.llm.device.type == "cuda":
-            raise HTTPException(400, "temperature > 0 is served by the CPU engine; the GPU runner decodes greedily")
+        """Refuse what the engine would refuse (e.g. penalties with SP prefill) with a 400."""
+        check = getattr(worker.llm, "_check_request", None)
+        if check is None:
+            return
+        try:
+            check([0], params)
+        except (NotImplementedError, ValueError) as e:
+            raise HTTPException(400, str(e))
+
+    def _usage_chunk(rid, created, obj, n_prompt, n_out):
+        return {"id": rid, "object": obj, "created": created, "model": name, "choices": [],
+                "usage": {"prompt_tokens": n_prompt, "completion_tokens": n_out, "total_tokens": n_prompt + n_out}}
+
+    def _prompt_text(p, ids):
+        return p if isinstance(p, str) else tok.decode([t for t in ids if t != tok.bos_token_id])
 
     def _prompt_ids(p):
         if isinstance(p, str):
@@ -392,30 +405,43 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
             raise HTTPException(400, str(e))
         _servable(params)
         prompts = body.get("prompt")
+        echo = bool(body.get("echo", False))
         if isinstance(prompts, list) and prompts and not isinstance(prompts[0], int):
             plist = [_prompt_ids(p) for p in prompts]
+            raw = list(prompts)
         else:
             plist = [_prompt_ids(prompts)]
+            raw = [prompts]
         rid, created = f"cmpl-{uuid.uuid4().hex[:24]}", int(time.time())
         if body.get("stream"):
             if len(plist) != 1 or params.n != 1:
                 raise HTTPException(400, "streaming serves one prompt and one completion per request")
             aq = run_request(plist[0], params)
+            usage = bool((body.get("stream_options") or {}).get("include_usage"))
 
             async def gen():
-                finish = None
+                finish, n_out = None, 0
                 ss = _StopStream(tok, params)
+                if echo:
+                    first = {"id": rid, "object": "text_completion", "created": created, "model": name,
+                             "choices": [{"index": 0, "text": _prompt_text(prompts if isinstance(prompts, (str, list))
+                                                                           else "", plist[0]),
+                                          "token_ids": [], "logprobs": None, "finish_reason": None}]}
+                    yield f"data: {json.dumps(first)}\n\n"
                 while finish is None:
                     ids, finish, lp = await aq.get()
                     if finish and finish.startswith("error:"):
                         yield f"data: {json.dumps({'error': finish[6:]})}\n\n"
                         break
+                    n_out += len(ids)
                     text = ss.push(ids, finish is not None) if params.stop else tok.decode(ids)
                     chunk = {"id": rid, "object": "text_completion", "created": created, "model": name,
                              "choices": [{"index": 0, "text": text, "token_ids": ids,
                                           "logprobs": completion_logprobs(ids, lp) if lp else None,
                                           "finish_reason": finish}]}
                     yield f"data: {json.dumps(chunk)}\n\n"
+                if usage:
+                    yield f"data: {json.dumps(_usage_chunk(rid, created, 'text_completion', len(plist[0]), n_out))}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(guard(gen(), aq), media_type="text/event-stream")
         qs = [run_request(p, c) for p in plist for c in copies(params)]
@@ -424,6 +450,9 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
             ids, finish, lps = await collect(aq)
             n_out += len(ids)
             text, hit = cut_at_stop(tok.decode(ids), params.stop, params.include_stop_str_in_output)
+            if echo:                                       # the prompt text before the completion
+                j = i // params.n
+                text = _prompt_text(raw[j], plist[j]) + text
             choices.append({"index": i, "text": text, "token_ids": ids, "finish_reason": finish,
                             "stop_reason": hit,
                             "logprobs": completion_logprobs(ids, lps) if params.logprobs is not None else None})
@@ -449,14 +478,17 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
         qs = [run_request(prompt, c) for c in copies(params)]
         aq = qs[0]
         if body.get("stream"):
+            usage = bool((body.get("stream_options") or {}).get("include_usage"))
+
             async def gen():
-                finish = None
+                finish, n_out = None, 0
                 first = True
                 ss = _StopStream(tok, params)
                 cps = _ChatParseStream(thinking and bool(reasoning_parser), bool(tool_call_parser)) \
                     if (reasoning_parser or tool_call_parser) else None
                 while finish is None:
                     ids, finish, _ = await aq.get()
+                    n_out += len(ids)
                     text = ss.push(ids, finish is not None) if params.stop else tok.decode(ids)
                     delta = cps.push(text, finish is not None) if cps is not None else {"content": text}
                     if first:
@@ -466,6 +498,8 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
                     chunk = {"id": rid, "object": "chat.completion.chunk", "created": created, "model": name,
                              "choices": [{"index": 0, "delta": delta, "finish_reason": fr}]}
                     yield f"data: {json.dumps(chunk)}\n\n"
+                if usage:
+                    yield f"data: {json.dumps(_usage_chunk(rid, created, 'chat.completion.chunk', len(prompt), n_out))}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(guard(gen(), aq), media_type="text/event-stream")
         choices, n_out = [], 0
