@@ -834,9 +834,10 @@ class NativeRunner:
         if self.tp_group is None:
             return logits
         from ..spec.device_sampler import gather_vocab
-        R, Vl = logits.shape
-        buf = self.ws.get("smp.vocab", (self.tp_size, R, Vl), logits.dtype)
-        return gather_vocab(logits, self.tp_group, buf)
+        # a plain allocation, not a workspace buffer: the sampling graph of a bucket may be
+        # captured after its greedy graph froze the bucket's workspace (inside a capture the
+        # tensor comes from that graph's own pool)
+        return gather_vocab(logits, self.tp_group)
 
     def _decode_body(self, st, sample: bool = False):
         C, k = self.C, self.k
