@@ -36,6 +36,7 @@ class BlockManager:
         self.by_key: Dict[tuple, int] = {}
         self.cached: "OrderedDict[int, None]" = OrderedDict()   # registered, unused (LRU order)
         self.stats = {"hit_blocks": 0, "lookups": 0, "evicted": 0}
+        self._cow_pending: Dict[str, int] = {}              # request -> copy source still referenced
 
     def blocks_needed(self, n_tokens: int) -> int:
         return -(-n_tokens // self.block_size)
@@ -121,13 +122,12 @@ class BlockManager:
         own = [self._pop_free() for _ in range(n - len(shared))]
         self.owned[req_id] = list(shared) + own
         self.stats["hit_blocks"] += len(hit)
-        self._cow_pending = getattr(self, "_cow_pending", {})
         self._cow_pending[req_id] = hit[-1]
         return list(shared) + own, len(hit) * self.block_size, (hit[-1], own[0])
 
     def copied(self, req_id: str) -> None:
         """The copy-on-write source of `req_id` has been copied: drop its extra reference."""
-        src = getattr(self, "_cow_pending", {}).pop(req_id, None)
+        src = self._cow_pending.pop(req_id, None)
         if src is not None:
             self._unref(src)
 
