@@ -105,3 +105,11 @@ def test_recipe_probes_over_http(tmp_path):
         srv.should_exit = True
         th.join(timeout=10)
         w.close()
+
+
+def test_shared_prefix_probe_reports_cache_hits():
+    from vllm_moet_b200.bench.harness import lint, resolve_recipe, run_recipe
+    res = run_recipe(resolve_recipe("tiny_cpu_prefix"))
+    row = [r for r in res["results"] if r["probe"] == "shared_prefix"][0]
+    assert row["hits"] == 3 and row["cold_ms"] > 0 and row["warm_ms"] > 0
+    assert not lint(res)

@@ -174,6 +174,22 @@ def run_recipe(path: str) -> dict:
             a = llm.generate([p], sp)[0].outputs[0].token_ids
             b = llm.generate([p], sp)[0].outputs[0].token_ids
             results.append({"probe": "coherence", "identical": a == b, "tokens": len(a)})
+        elif kind == "shared_prefix":
+            # requests sharing a long prefix: time to first token of the first (cold) and of
+            # the later ones (prefix cache warm when the engine has it on)
+            pre = prompt(pr["prefix_len"])
+            ttft = []
+            for i in range(pr["requests"]):
+                p = pre + prompt(pr["suffix_len"])
+                t0 = time.perf_counter()
+                llm.generate([p], SamplingParams(max_tokens=1, ignore_eos=True))
+                _sync(llm.device)
+                ttft.append((time.perf_counter() - t0) * 1e3)
+            bm = getattr(llm, "blocks", None)
+            hits = (bm.stats["hit_blocks"] if bm is not None and getattr(bm, "prefix_caching", False)
+                    else getattr(llm.runner, "prefix_stats", {}).get("hits"))
+            results.append({"probe": "shared_prefix", "prefix_len": pr["prefix_len"], "cold_ms": ttft[0],
+                            "warm_ms": sum(ttft[1:]) / max(1, len(ttft) - 1), "hits": hits})
         else:
             raise ValueError(f"unknown probe kind {kind!r}")
     dev = torch.cuda.get_device_name(0) if torch.cuda.is_available() and llm.device.type == "cuda" else "cpu"
