@@ -60,3 +60,28 @@ def test_ep2_forward_matches_single_rank():
     assert [(r[2], r[3]) for r in res] == [(0, 4), (4, 4)]
     for err, scale, _, _ in res:
         assert err <= 1e-4 * max(scale, 1.0), (err, scale)
+
+
+def _tp_prefix_chunked(rank, world):
+    import torch.distributed as dist
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256, tensor_parallel_size=world,
+              tp_group=dist.group.WORLD, tp_rank=rank, enable_prefix_caching=True, prefix_block_size=8,
+              enable_chunked_prefill=True, max_num_batched_tokens=8)
+    pre = list(range(3, 35))
+    sp = SamplingParams(max_tokens=8, ignore_eos=True, presence_penalty=0.5)
+    outs = [llm.generate([pre + [40 + i]], sp)[0].outputs[0].token_ids for i in range(2)]
+    return outs, llm.runner.prefix_stats["hits"]
+
+
+def test_tp2_prefix_cache_chunked_prefill_and_penalties_match_one_rank():
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    res = run_ranks(_tp_prefix_chunked, 2)
+    one = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256)
+    pre = list(range(3, 35))
+    sp = SamplingParams(max_tokens=8, ignore_eos=True, presence_penalty=0.5)
+    want = [one.generate([pre + [40 + i]], sp)[0].outputs[0].token_ids for i in range(2)]
+    for outs, hits in res:
+        assert outs == want and hits == 1
