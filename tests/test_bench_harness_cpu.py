@@ -13,7 +13,7 @@ def test_tiny_recipe_run_lint_render(tmp_path):
     assert res["source_fingerprint"] == source_fingerprint()
     assert not lint(res, str(rec))
     kinds = [r["probe"] for r in res["results"]]
-    assert kinds.count("decode") == 2 and {"probe": "coherence", "identical": True, "tokens": 8} in res["results"]
+    assert kinds.count("decode") == 2 and {"probe": "coherence", "identical": True, "tokens": 8, "degenerate": False} in res["results"]
     table = render([res])
     assert "| tiny_cpu | cpu | coherence | 8 tokens | identical |" in table
     rec.write_text(rec.read_text() + "\n# edited\n")
@@ -63,7 +63,8 @@ def test_every_recipe_is_well_formed():
         rec = yaml.safe_load(open(os.path.join(RECIPE_DIR, fn)))
         assert rec["name"] == fn[:-5], fn
         assert set(rec.get("engine", {})) <= params | {"device"}, (fn, set(rec["engine"]) - params)
-        assert all(p["kind"] in ("decode", "prefill", "coherence") for p in rec["probes"]), fn
+        assert all(p["kind"] in ("decode", "prefill", "coherence", "shared_prefix", "needle", "arithmetic",
+                                 "quality") for p in rec["probes"]), fn
         assert set(rec.get("parallel") or {}) <= {"tp", "pp", "ep"}, fn
 
 
@@ -112,4 +113,18 @@ def test_shared_prefix_probe_reports_cache_hits():
     res = run_recipe(resolve_recipe("tiny_cpu_prefix"))
     row = [r for r in res["results"] if r["probe"] == "shared_prefix"][0]
     assert row["hits"] == 3 and row["cold_ms"] > 0 and row["warm_ms"] > 0
+    assert not lint(res)
+
+
+def test_quality_needle_and_arithmetic_probes():
+    """The quality probe pairs the recipe's engine (MTP k=2) with a baseline (no
+    speculation) against the oracle: both exact, so McNemar finds nothing and the gates
+    pass; needle and arithmetic report structured results (random weights fail them)."""
+    from vllm_moet_b200.bench.harness import lint, resolve_recipe, run_recipe
+    res = run_recipe(resolve_recipe("tiny_cpu_quality"))
+    q = [r for r in res["results"] if r["probe"] == "quality"][0]
+    assert q["pass"] and q["vs_baseline"]["acc_cand"] == q["vs_baseline"]["acc_base"] == 1.0
+    a = [r for r in res["results"] if r["probe"] == "arithmetic"][0]
+    n = [r for r in res["results"] if r["probe"] == "needle"][0]
+    assert a["of"] == 4 and 0 <= a["score"] <= 4 and n["cases"][0]["words"] == 60
     assert not lint(res)

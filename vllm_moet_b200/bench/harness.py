@@ -171,9 +171,17 @@ def run_recipe(path: str) -> dict:
         elif kind == "coherence":
             p = prompt(pr["prompt_len"])
             sp = SamplingParams(max_tokens=pr["tokens"], ignore_eos=True)
-            a = llm.generate([p], sp)[0].outputs[0].token_ids
+            a = llm.generate([p], sp)[0].outputs[0]
             b = llm.generate([p], sp)[0].outputs[0].token_ids
-            results.append({"probe": "coherence", "identical": a == b, "tokens": len(a)})
+            from .stats import degenerate
+            results.append({"probe": "coherence", "identical": a.token_ids == b, "tokens": len(a.token_ids),
+                            "degenerate": degenerate(a.text)})
+        elif kind == "needle":
+            results.append(_needle(llm, pr))
+        elif kind == "arithmetic":
+            results.append(_arithmetic(llm, pr))
+        elif kind == "quality":
+            results.append(_quality(llm, rec, pr, prompt))
         elif kind == "shared_prefix":
             # requests sharing a long prefix: time to first token of the first (cold) and of
             # the later ones (prefix cache warm when the engine has it on)
@@ -197,6 +205,66 @@ def run_recipe(path: str) -> dict:
             "source_fingerprint": source_fingerprint(), "device": dev, "results": results,
             "world": int(os.environ.get("WORLD_SIZE", "1")), "parallel": rec.get("parallel") or {},
             "time": time.strftime("%Y-%m-%dT%H:%M:%SZ", time.gmtime())}
+
+
+_FILLER = ("river stone lantern copper meadow violet harbor quiet thunder maple orbit canvas velvet "
+           "pepper glacier saddle willow ember falcon marble").split()
+_SECRET = "cobalt-heron-7319"
+_ARITH = [("What is 219 * 37? Reply with only the number.", 8103),
+          ("What is 64 * 58? Reply with only the number.", 3712),
+          ("What is 1200 + 345 + 78 + 9? Reply with only the number.", 1632),
+          ("What is 9081 - 4567? Reply with only the number.", 4514)]
+
+
+def _needle(llm, pr) -> dict:
+    """A passphrase at `depth` inside `words` filler words; pass if the answer holds it."""
+    import random
+    from ..engine.sampling_params import SamplingParams
+    cases = []
+    for n in pr.get("words", [200]):
+        rnd = random.Random(11)
+        filler = [rnd.choice(_FILLER) for _ in range(n)]
+        at = int(n * pr.get("depth", 0.5))
+        text = " ".join(filler[:at]) + f"\n\nThe vault passphrase is {_SECRET}.\n\n" + " ".join(filler[at:])
+        msg = [{"role": "user", "content": text + "\n\nWhat is the vault passphrase? Reply with it only."}]
+        out = llm.chat(msg, SamplingParams(max_tokens=pr.get("max_tokens", 24)))[0].outputs[0].text
+        cases.append({"words": n, "pass": _SECRET in out})
+    return {"probe": "needle", "cases": cases, "all_pass": all(c["pass"] for c in cases)}
+
+
+def _arithmetic(llm, pr) -> dict:
+    import re
+    from ..engine.sampling_params import SamplingParams
+    rows = []
+    for q, gold in _ARITH:
+        out = llm.chat([{"role": "user", "content": q}], SamplingParams(max_tokens=pr.get("max_tokens", 32)))
+        nums = re.findall(r"-?\d+", out[0].outputs[0].text.replace(",", ""))
+        got = int(nums[-1]) if nums else None
+        rows.append({"gold": gold, "got": got, "ok": got == gold})
+    return {"probe": "arithmetic", "score": sum(r["ok"] for r in rows), "of": len(rows), "rows": rows}
+
+
+def _quality(llm, rec, pr, prompt) -> dict:
+    """Paired A/B of the recipe's engine against `baseline` engine settings: an item is
+    correct when the engine's greedy tokens equal the fp32 oracle's; McNemar and the
+    paired token statistics decide the recipe's `gates`."""
+    from ..engine.llm import LLM
+    from ..engine.sampling_params import SamplingParams
+    from ..models import reference
+    from .stats import compare, passes
+    eng = dict(rec.get("engine", {}), **pr.get("baseline", {}))
+    base = LLM(rec["model"], **eng, **_parallel(rec), **rec.get("overrides", {}))
+    sp = SamplingParams(max_tokens=pr["tokens"], ignore_eos=True)
+    rows_c, rows_b = {}, {}
+    for i in range(pr["items"]):
+        p = prompt(pr["prompt_len"])
+        want = reference.greedy_generate(llm.mw, p, pr["tokens"])
+        for eng_, rows in ((llm, rows_c), (base, rows_b)):
+            got = eng_.generate([p], sp)[0].outputs[0].token_ids
+            rows[f"item{i}"] = {"correct": got == want, "tokens": len(got)}
+    cmp_ = compare(rows_b, rows_c)
+    return {"probe": "quality", "items": pr["items"], "vs_baseline": cmp_,
+            "pass": passes(cmp_, pr.get("gates", {}))}
 
 
 def lint(result: dict, recipe_path: str = None) -> List[str]:
