@@ -91,6 +91,7 @@ def test_completions_match_engine(server):
     assert "moet_time_to_first_token_seconds_count" in m and "moet_e2e_request_latency_seconds_bucket" in m
     count = [ln for ln in m.splitlines() if ln.startswith("moet_e2e_request_latency_seconds_count")][0]
     assert float(count.split()[-1]) >= 1
+    assert "moet_decode_steps_total" in m and "moet_accepted_draft_tokens_total" in m
 
 
 def test_streaming_and_chat(server):

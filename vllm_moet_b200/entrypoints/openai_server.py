@@ -42,7 +42,7 @@ class EngineWorker:
         self.max_batch = max_batch
         self.q: "queue.Queue" = queue.Queue()
         self.stats = {"requests": 0, "prompt_tokens": 0, "generated_tokens": 0, "batches": 0, "joined": 0,
-                      "aborted": 0}
+                      "aborted": 0, "decode_steps": 0, "accepted_draft_tokens": 0}
         self._ids = itertools.count()
         self._aborts: set = set()
         self._lock = threading.Lock()
@@ -116,9 +116,22 @@ class EngineWorker:
             outs = self.llm.generate(prompts, params, callbacks=[b[3] for b in batch], request_ids=rids,
                                      between_steps=self._between)
             self.stats["generated_tokens"] += sum(len(o.outputs[0].token_ids) for o in outs)
+            self._engine_counters()
         except Exception as e:  # noqa: BLE001 - report to every waiting request
             for b in batch:
                 b[3]([], "error:" + str(e))
+
+    def _engine_counters(self):
+        """Speculative-decoding and prefix-cache counters of the run that just ended."""
+        st = getattr(self.llm, "stats", {}) or {}
+        self.stats["decode_steps"] += int(st.get("steps") or 0)
+        self.stats["accepted_draft_tokens"] += int(st.get("accepted") or 0)
+        bm = getattr(self.llm, "blocks", None)
+        if bm is not None and getattr(bm, "prefix_caching", False):
+            self.stats["prefix_cache_hit_blocks"] = bm.stats["hit_blocks"]
+        ps = getattr(getattr(self.llm, "runner", None), "prefix_stats", None)
+        if ps is not None:
+            self.stats["prefix_cache_hits"] = ps["hits"]
 
     def close(self):
         self.q.put(None)
