@@ -338,3 +338,43 @@ def test_echo_and_stream_usage(server):
     events = [json.loads(ln[6:]) for ln in r.iter_lines(decode_unicode=True)
               if ln.startswith("data: ") and ln != "data: [DONE]"]
     assert events[-1]["usage"]["completion_tokens"] == 3 and events[-1]["usage"]["prompt_tokens"] > 0
+
+
+def test_server_with_prefix_cache_chunked_prefill_and_dspark():
+    """The server over an engine with prefix caching, chunked prefill and (context-free)
+    DSpark drafting:
+    completions sharing a prefix are the target's greedy tokens; the metrics count hits."""
+    import uvicorn
+    from vllm_moet_b200.engine.llm import LLM
+    from vllm_moet_b200.entrypoints.openai_server import EngineWorker, build_app
+    from vllm_moet_b200.models import reference
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=0, max_model_len=256, speculative_method="dspark",
+              dspark={"block": 3, "tau": 0.0, "budget_frac": 1.0, "model": "simple"}, enable_prefix_caching=True,
+              prefix_block_size=8,
+              enable_chunked_prefill=True, max_num_batched_tokens=8)
+    w = EngineWorker(llm, "tiny")
+    port = _free_port()
+    srv = uvicorn.Server(uvicorn.Config(build_app(w), host="127.0.0.1", port=port, log_level="warning"))
+    th = threading.Thread(target=srv.run, daemon=True)
+    th.start()
+    url = f"http://127.0.0.1:{port}"
+    try:
+        for _ in range(100):
+            try:
+                if requests.get(url + "/health", timeout=1).ok:
+                    break
+            except requests.ConnectionError:
+                time.sleep(0.1)
+        pre = list(range(3, 27))
+        for tail in ([50, 51], [60]):
+            p = pre + tail
+            r = requests.post(url + "/v1/completions", json={"prompt": p, "max_tokens": 6, "ignore_eos": True},
+                              timeout=120).json()
+            assert r["choices"][0]["token_ids"] == reference.greedy_generate(llm.mw, p, 6)
+        m = requests.get(url + "/metrics").text
+        hits = [ln for ln in m.splitlines() if ln.startswith("moet_prefix_cache_hits_total")]
+        assert hits and float(hits[0].split()[-1]) == 1      # the second prompt reused 24 cached tokens
+    finally:
+        srv.should_exit = True
+        th.join(timeout=10)
+        w.close()
