@@ -94,3 +94,24 @@ def test_dflash_is_the_context_drafter_without_markov_heads():
     d.extend(c, aux, 0, 4)
     dr, base, surv = d.propose_one(c, 9, 4)
     assert dr.tolist() == base.argmax(-1).tolist() and bool((surv == 1).all())
+
+
+def test_prefix_cache_restores_the_dspark_context():
+    """Prefix caching with the DSpark context drafter: the cached prefix carries the
+    drafter's window at its end, so a hit drafts exactly as a cold run (same steps and
+    acceptance) and still emits the target's greedy tokens; chunked prefill cuts the
+    context at every block boundary the same way."""
+    kw = dict(device="cpu", num_speculative_tokens=0, max_model_len=256, speculative_method="dspark",
+              dspark={"block": 3, "tau": 0.0, "budget_frac": 1.0, "window": 12})
+    cold = LLM("tiny-moe", **kw)
+    warm = LLM("tiny-moe", enable_prefix_caching=True, prefix_block_size=8, enable_chunked_prefill=True,
+               max_num_batched_tokens=5, **kw)
+    pre = list(range(3, 27))
+    sp = SamplingParams(max_tokens=9, ignore_eos=True)
+    for tail in ([40, 41], [50]):
+        p = pre + tail
+        a = cold.generate([p], sp)[0].outputs[0].token_ids
+        b = warm.generate([p], sp)[0].outputs[0].token_ids
+        assert a == b == ref.greedy_generate(cold.mw, p, 9)
+        assert warm.stats["accepted"] == cold.stats["accepted"]
+    assert warm.runner.prefix_stats["hits"] == 1

@@ -136,7 +136,9 @@ class TorchRunner:
         # invariant: main K/V covers [0, done), MTP K/V covers [0, done - 1) (the MTP entry of
         # position p needs token p + 1); hprev is the hidden state at done - 1
         self.partial[r] = dict(prompt=list(prompt), sp=sp, smp=self._sample_state(sp), main=main, mtp=mtp, done=m,
-                               hprev=hprev, logits=logits, bound={}, chunks=0)
+                               hprev=hprev, logits=logits, bound={}, chunks=0, dsnap={})
+        if ent is not None and ent.get("dctx") is not None:      # the DSpark context of the prefix
+            self.partial[r]["dctx"] = self._dctx_copy(ent["dctx"])
 
     def _chunk(self, r, budget):
         st = self.partial[r]
@@ -148,8 +150,17 @@ class TorchRunner:
         ls, hs = ref.forward(self.mw, torch.tensor(prompt[s:e], device=self.dev),
                              torch.arange(s, e, device=self.dev), self.cs, main, aux=aux)
         if cd is not None:
+            # extend the drafter's context, snapshotting it at every block boundary for the
+            # prefix cache (its window ends there)
             st.setdefault("dctx", cd.new_context())
-            cd.extend(st["dctx"], aux, s, e - s)
+            b, at = self.prefix_block, s
+            cuts = [m for m in range(-(-(s + 1) // b) * b, min(e, n - 1) + 1, b)] if b else []
+            for m in cuts + [e]:
+                if m > at:
+                    cd.extend(st["dctx"], {li: a[at - s:m - s] for li, a in aux.items()}, at, m - at)
+                    at = m
+                if m in cuts:
+                    st["dsnap"][m] = self._dctx_copy(st["dctx"])
         st["logits"].append(ls)
         st["chunks"] += 1
         b = self.prefix_block
@@ -176,7 +187,7 @@ class TorchRunner:
             ml, mh = ref.mtp_forward(self.mw, hid, nxt, torch.arange(p0, n, device=self.dev), self.cs, mtp)
             drafts = self._chain_drafts(ml, mh, n, mtp)
         for m, h in st["bound"].items():
-            self._prefix_put(prompt[:m], main, mtp, h, logits[:m])
+            self._prefix_put(prompt[:m], main, mtp, h, logits[:m], st["dsnap"].get(m))
         self.rows[r] = dict(main=main, mtp=mtp, tokens=[tgt] + drafts, pos=n, sample=smp, hid=hid[-1],
                             sp=st["sp"], prompt=prompt, out=[tgt], dctx=st.get("dctx"))
         del self.partial[r]
@@ -227,24 +238,30 @@ class TorchRunner:
         return d if hasattr(d, "extend") else None
 
     def _prefix_lookup(self, prompt):
-        """-> (m, entry) of the longest cached block-aligned prefix shorter than the prompt.
-        (Not with a context drafter: its context K/V of the prefix are not cached.)"""
-        if not self.prefix_block or self.sp_group is not None or self.dcp_group is not None or \
-                self._context_drafter() is not None:
+        """-> (m, entry) of the longest cached block-aligned prefix shorter than the prompt
+        (with a context drafter, only entries that hold its context)."""
+        if not self.prefix_block or self.sp_group is not None or self.dcp_group is not None:
             return 0, None
+        need_ctx = self._context_drafter() is not None
         self.prefix_stats["lookups"] += 1
         b = self.prefix_block
         for m in range((len(prompt) - 1) // b * b, 0, -b):
             ent = self.prefix_cache.get(tuple(prompt[:m]))
-            if ent is not None:
+            if ent is not None and (not need_ctx or ent.get("dctx") is not None):
                 self.prefix_cache.move_to_end(tuple(prompt[:m]))
                 self.prefix_stats["hits"] += 1
                 self.prefix_stats["hit_tokens"] += m
                 return m, ent
         return 0, None
 
-    def _prefix_put(self, key, main, mtp, hid, logits):
-        """Cache one block-aligned prefix (`hid`: the hidden state at its last position)."""
+    @staticmethod
+    def _dctx_copy(c):
+        from ..models.dspark_model import DSparkContext
+        return DSparkContext(list(c.k), list(c.v), c.end)
+
+    def _prefix_put(self, key, main, mtp, hid, logits, dctx=None):
+        """Cache one block-aligned prefix (`hid`: the hidden state at its last position;
+        `dctx`: the DSpark context at its end)."""
         key, m = tuple(key), len(key)
         if key in self.prefix_cache:
             self.prefix_cache.move_to_end(key)
@@ -252,7 +269,7 @@ class TorchRunner:
         pm, pq = self._kv_copy(main), self._kv_copy(mtp)
         pm.truncate(m)
         pq.truncate(m - 1)
-        self.prefix_cache[key] = dict(main=pm, mtp=pq, hid=hid, logits=logits)
+        self.prefix_cache[key] = dict(main=pm, mtp=pq, hid=hid, logits=logits, dctx=dctx)
         while len(self.prefix_cache) > self.prefix_entries:
             self.prefix_cache.popitem(last=False)
 
