@@ -123,3 +123,20 @@ def test_batched_processing_equals_per_row_processing():
         want = process_logits(logits[b], sps[b], prompts[b], outs[b], drafts[b].tolist())
         assert torch.allclose(got[b], want, atol=1e-5), b
     assert torch.equal(got[1], logits[1])
+
+
+def _tp_logprob_rows(rank, world):
+    import types
+    import torch.distributed as dist
+    from vllm_moet_b200.engine.llm import LLM
+    full = torch.arange(6 * 8, dtype=torch.float32).view(6, 8)
+    fake = types.SimpleNamespace(_tp_group=dist.group.WORLD, device=types.SimpleNamespace(type="cuda"))
+    got = LLM._full_logits(fake, full[:, rank * 4:(rank + 1) * 4].clone())
+    return torch.equal(got, full)
+
+
+def test_logprob_rows_under_tp_are_whole_vocabulary():
+    """GPU logprobs under TP: the verify / prefill rows are the ranks' vocab shards
+    gathered back into whole rows."""
+    from mp_util import run_ranks
+    assert run_ranks(_tp_logprob_rows, 2) == [True, True]

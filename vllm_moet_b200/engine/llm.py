@@ -392,8 +392,6 @@ class LLM:
         return self.generate(prompts, sampling_params)
 
     def _check_request(self, t, sp):
-        if sp.logprobs is not None and self.device.type == "cuda" and self._tp_group is not None:
-            raise NotImplementedError("logprobs under tensor parallelism: each rank holds a vocab shard")
         if sp.prompt_logprobs is not None and self.device.type == "cuda":
             raise NotImplementedError("prompt_logprobs: the GPU prefill keeps only each prompt's last logits")
         if sp.processes_logits or sp.min_p > 0:
@@ -749,8 +747,8 @@ class LLM:
             t_decode += time.perf_counter() - t0
             runner.check_status("decode step")
             steps += 1
-            dl = runner.main_logits(B) if any(r is not None and r.params.logprobs is not None for r in rows) \
-                else None
+            dl = self._full_logits(runner.main_logits(B)) \
+                if any(r is not None and r.params.logprobs is not None for r in rows) else None
             if getattr(st, "proc", None) is not None:          # generated-token counts for the penalties
                 cr, ct = [], []
                 for i, r in enumerate(rows):
@@ -782,13 +780,26 @@ class LLM:
                 self.blocks.register(r.rid, r.prompt)
         now = time.perf_counter()
         want_lp = any(r.params.logprobs is not None for r in adm)
-        pl = runner.ws_prefill.get("main.logits", (len(adm), self.cfg.vocab), torch.float32) if want_lp else None
+        pl = self._full_logits(runner.ws_prefill.get("main.logits", (len(adm), self._vocab_local()), torch.float32)) \
+            if want_lp else None
         if getattr(st, "proc", None) is not None:
             st.count_tokens([r.row for r in adm], firsts)
         for j, (r, f) in enumerate(zip(adm, firsts)):
             r.t_first = now
             if self._emit(r, [f], pl[j:j + 1] if pl is not None else None):
                 self._finish_row(r, rows)
+
+    def _vocab_local(self) -> int:
+        head = getattr(getattr(self, "mw", None), "lm_head", None)
+        return head.shape[0] if head is not None and self._tp_group is not None else self.cfg.vocab
+
+    def _full_logits(self, lg):
+        """Logprobs under TP: the ranks' vocab shards gathered into whole rows (every rank
+        runs the same host loop, so the collective lines up)."""
+        if lg is None or self._tp_group is None or self.device.type != "cuda":
+            return lg
+        from ..spec.device_sampler import gather_vocab
+        return gather_vocab(lg.contiguous(), self._tp_group)
 
     def _gpu_chunks(self, prefilling, st, bt_host, rows):
         """Chunked prefill on the GPU runner: the step's token budget goes to the decoding
