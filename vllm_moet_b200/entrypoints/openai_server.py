@@ -564,10 +564,10 @@ def build_parser():
     ap.add_argument("--decode-context-parallel-size", type=int, default=1)
     ap.add_argument("--enable-expert-parallel", action="store_true")
     ap.add_argument("--enable-prefix-caching", action="store_true",
-                    help="reuse the K/V of shared block-aligned prompt prefixes (CPU engine)")
-    ap.add_argument("--block-size", type=int, default=16, help="prefix-cache block, in tokens")
+                    help="reuse the K/V of shared block-aligned prompt prefixes")
+    ap.add_argument("--block-size", type=int, default=16, help="prefix-cache block of the CPU engine, in tokens (GPU: 64-token KV blocks)")
     ap.add_argument("--enable-chunked-prefill", action="store_true",
-                    help="prefill long prompts a token budget per step beside the decoding rows (CPU engine)")
+                    help="prefill long prompts a token budget per step beside the decoding rows")
     ap.add_argument("--max-num-batched-tokens", type=int, default=None, help="per-step token budget (chunked prefill)")
     ap.add_argument("--gpus", default=None, help="GPU ids for the replicas of --data-parallel-size ('cpu': none)")
     ap.add_argument("--reasoning-parser", default="deepseek_v4", choices=_PARSERS)
