@@ -525,6 +525,8 @@ extern "C" int moet_build_pairs_noalloc(const int* topk_ids, int num_tokens, int
   const long long R = (long long)num_tokens * top_k;
   if (R > MOET_NOALLOC_MAX_ROUTINGS) return MOET_NOALLOC_ETOOBIG;
   if ((long long)max_pairs < R / rows_per_pair + std::min<long long>(num_experts, R)) return MOET_NOALLOC_EINVAL;
+  // the kernel writes each pair record as one 16-byte store
+  if ((reinterpret_cast<uintptr_t>(pairs) & 15) != 0) return MOET_NOALLOC_EINVAL;
   int dev = 0;
   cudaError_t rc = cudaGetDevice(&dev);
   if (rc != cudaSuccess) return (int)rc;

@@ -22,7 +22,8 @@ extern "C" {
 
 // Return codes (besides these, a positive value is a cudaError_t).
 #define MOET_NOALLOC_OK 0
-#define MOET_NOALLOC_EINVAL (-1)   // bad argument (null pointer, k/E/rows out of range, max_pairs too small)
+#define MOET_NOALLOC_EINVAL (-1)   // bad argument (null pointer, k/E/rows out of range, max_pairs too
+                                   // small, pairs not 16-byte aligned)
 #define MOET_NOALLOC_ETOOBIG (-2)  // num_tokens * top_k exceeds MOET_NOALLOC_MAX_ROUTINGS
 
 // Groups the num_tokens*top_k routings in topk_ids [num_tokens, top_k]
@@ -31,9 +32,12 @@ extern "C" {
 //   sorted_tok [R]        token of each expert-sorted row
 //   pos_of     [R]        routing t*top_k+j -> sorted row
 //   pairs      [max_pairs][4] {expert, first sorted row, n rows, 0};
-//                          max_pairs >= R/rows_per_pair + min(num_experts, R)
+//                          max_pairs >= R/rows_per_pair + min(num_experts, R);
+//                          16-byte aligned (each record is one 16-byte store)
 //   n_pairs    [1]        number of pairs written
-//   status     [1]        set to 1 if an expert id is out of range
+//   status     [1]        caller-zeroed: the kernel only ever sets it (to 1
+//                          when an expert id is out of range; such a routing
+//                          is counted under expert 0) and never clears it
 // Enqueued on `stream`; returns before the kernel finishes.
 //
 // Set-up: the first call on each device (with that device current) looks up

@@ -81,3 +81,20 @@ def test_random_sequences_keep_the_invariants():
         bm.release(rid)
     bm.check_invariants()
     assert bm.num_free == 59
+
+
+def test_colliding_digest_never_maps_another_prompts_blocks(monkeypatch):
+    """Even with a digest that collides for every chain, a lookup only hits blocks whose
+    tokens equal the prompt's (and whose whole prefix matched before them)."""
+    monkeypatch.setattr(BlockManager, "_digest", staticmethod(lambda prev, toks: b"same"))
+    bm = BlockManager(40, block_size=B, prefix_caching=True)
+    p1 = [1, 2, 3, 4, 5, 6, 7, 8, 9]
+    bm.allocate_with_prefix("a", 12, p1)
+    bm.register("a", p1)
+    p2 = [9, 9, 9, 9, 5, 6, 7, 8, 9]                  # block 1 equal, block 0 not: no hit at all
+    _, m, cow = bm.allocate_with_prefix("b", 12, p2)
+    assert m == 0 and cow is None
+    p3 = [1, 2, 3, 4, 5, 6, 7, 0, 9]                  # block 0 equal, block 1 not: only block 0
+    _, m, _ = bm.allocate_with_prefix("c", 12, p3)
+    assert m == 4
+    bm.check_invariants()

@@ -85,3 +85,23 @@ def test_tp2_prefix_cache_chunked_prefill_and_penalties_match_one_rank():
     want = [one.generate([pre + [40 + i]], sp)[0].outputs[0].token_ids for i in range(2)]
     for outs, hits in res:
         assert outs == want and hits == 1
+
+
+def _tp_unseeded_sampling(rank, world):
+    import random
+
+    import torch.distributed as dist
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    random.seed(1000 + rank)      # each rank's Python RNG differs, as OS seeding makes it
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=256,
+              tensor_parallel_size=world, tp_group=dist.group.WORLD, tp_rank=rank)
+    sp = SamplingParams(max_tokens=12, ignore_eos=True, temperature=1.0)
+    return [o.outputs[0].token_ids for o in llm.generate([[5, 6, 7, 8], [9, 10, 11]], sp)]
+
+
+def test_tp2_unseeded_sampling_agrees_across_ranks():
+    """Unseeded temperature > 0 requests draw one seed per request on TP rank 0, shared by
+    every rank, so both ranks emit the same tokens."""
+    a, b = run_ranks(_tp_unseeded_sampling, 2)
+    assert a == b

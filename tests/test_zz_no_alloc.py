@@ -94,3 +94,39 @@ def test_noalloc_rejects_oversize_and_bad_args(lib):
     assert int(outs[3]) == 0 and bool((outs[0] == -7).all())  # nothing was launched
     small = torch.zeros(4, 8, dtype=torch.int32, device=DEV)
     assert _call(fn, small, 256, 8, _outputs(32, 1)) == -1   # pairs buffer too small
+
+
+def test_noalloc_rejects_misaligned_pairs(lib):
+    """The pair records are 16-byte stores: a pairs pointer off a 16-byte boundary is refused
+    on the host before anything is launched."""
+    _, fn = lib
+    ids = torch.zeros(4, 8, dtype=torch.int32, device=DEV)
+    stok, posof, pairs, npairs, status = _outputs(32, 64)
+    flat = pairs.view(-1)
+    rc = fn(ids.data_ptr(), 4, 8, 256, 8, stok.data_ptr(), posof.data_ptr(), flat[1:].data_ptr(), 63,
+            npairs.data_ptr(), status.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rc == -1
+    assert int(npairs) == 0 and bool((pairs == -7).all())
+
+
+def test_noalloc_out_of_range_id_sets_caller_zeroed_status(lib):
+    """An expert id >= num_experts sets status to 1, as build_pairs does, and the routing is
+    counted under expert 0; status is never cleared by the call (the caller zeroes it)."""
+    mod, fn = lib
+    E, MB = 16, 8
+    ids = torch.tensor([[3, 20], [0, 5]], dtype=torch.int32, device=DEV)
+    R, P = 4, 4 // MB + min(E, 4)
+    ref = _outputs(R, P)
+    rank = torch.empty(R, dtype=torch.int32, device=DEV)
+    mod.build_pairs(ids, E, MB, rank, ref[0], ref[1], ref[2], ref[3], ref[4])
+    outs = _outputs(R, P)
+    assert _call(fn, ids, E, MB, outs) == 0
+    assert int(outs[4]) == 1 and int(ref[4]) == 1
+    assert int(outs[3]) == int(ref[3]) == 3          # experts 0 (two rows), 3 and 5
+    # a second, valid call leaves the caller's status word as it found it
+    ok = torch.tensor([[1, 2]], dtype=torch.int32, device=DEV)
+    outs2 = _outputs(2, 2 // MB + 2)
+    outs2[4].fill_(1)
+    assert _call(fn, ok, E, MB, outs2) == 0
+    assert int(outs2[4]) == 1 and int(outs2[3]) == 2

@@ -685,7 +685,8 @@ class NativeRunner:
         """Copy one KV block (every layer's latent cache, the MTP layer's and the indexer's):
         the copy-on-write step of prefix sharing."""
         for t in list(self.kv) + list(getattr(self, "idx_kv", None) or []):
-            t[dst].copy_(t[src])
+            if t is not None:     # idx_kv holds None for layers without an indexer
+                t[dst].copy_(t[src])
 
     def prefill(self, prompts: list, block_tables: list, seq_rows: list, state, sample: bool = False,
                 starts: Optional[list] = None):

@@ -7,7 +7,7 @@ and no host round trip for paging.  Blocks return to the free list when the
 request finishes.
 
 Prefix caching (``enable_prefix_caching``): a block whose 64 positions are all
-prompt tokens is registered under a chain hash (the previous block's key and its
+prompt tokens is registered under a chain key (a SHA-256 digest of the earlier blocks and its
 own tokens), so a later prompt with the same leading blocks maps them into its
 table instead of recomputing them.  Shared blocks are reference-counted; a
 registered block whose last user finished stays cached, reclaimable
@@ -19,6 +19,8 @@ own.
 """
 from __future__ import annotations
 
+import hashlib
+import struct
 from collections import OrderedDict
 from typing import Dict, List, Optional, Sequence, Tuple
 
@@ -58,12 +60,23 @@ class BlockManager:
         return need <= avail
 
     # ------------------------------------------------------------------ prefix keys
+    @staticmethod
+    def _digest(prev: bytes, tokens: tuple) -> bytes:
+        """SHA-256 of the chain so far and one block's tokens (collision resistant: a client
+        cannot craft a prompt whose key lands on another prompt's cached blocks)."""
+        h = hashlib.sha256(prev)
+        h.update(struct.pack(f"<{len(tokens)}q", *tokens))
+        return h.digest()
+
     def _keys(self, prompt: Sequence[int]) -> List[tuple]:
-        """Chain keys of the prompt's full blocks."""
-        b, keys, prev = self.block_size, [], None
+        """Chain keys of the prompt's full blocks: (digest of every earlier block, the block's
+        own tokens).  The tokens are part of the key, so a hit compares them exactly; the
+        digest ties the block to its whole prefix."""
+        b, keys, prev = self.block_size, [], b""
         for i in range(len(prompt) // b):
-            prev = (hash((prev, tuple(prompt[i * b:(i + 1) * b]))), i)
-            keys.append(prev)
+            toks = tuple(int(t) for t in prompt[i * b:(i + 1) * b])
+            keys.append((prev, toks))
+            prev = self._digest(prev, toks)
         return keys
 
     def _match(self, prompt: Optional[Sequence[int]]) -> Tuple[List[int], List[tuple]]:

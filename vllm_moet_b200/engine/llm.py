@@ -851,12 +851,17 @@ class LLM:
                 st.set_sampling([r.row for r in adm], [0.0] * len(adm), [0] * len(adm), [1.0] * len(adm),
                                 [0.0] * len(adm), [0] * len(adm))
             return False
-        import random
         ps = [r.params for r in adm]
+        drawn = self._shared_seeds(len(ps))
         st.set_sampling([r.row for r in adm], [p.temperature for p in ps], [p.top_k for p in ps],
                         [p.top_p for p in ps], [p.min_p for p in ps],
-                        [p.seed if p.seed is not None else random.getrandbits(62) for p in ps])
+                        [p.seed if p.seed is not None else d for p, d in zip(ps, drawn)])
         return True
+
+    def _shared_seeds(self, n: int) -> list:
+        """n random seeds, equal on every rank of the tensor-parallel group."""
+        from .sampling_params import shared_seeds
+        return shared_seeds(n, self._tp_group, self.device)
 
     def _delta_step(self, st, B, graph, kp1):
         """After a decode step: feed routing to the delta tier's frequency policy and,

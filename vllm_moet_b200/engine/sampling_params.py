@@ -116,3 +116,23 @@ def logprob_entries(logits, tokens, top_n: int):
                 d.setdefault(int(tt), float(vv))
         out.append(d)
     return out
+
+
+def shared_seeds(n: int, group=None, device=None) -> list:
+    """n random seeds for unseeded sampling requests, the same on every rank of `group`.
+
+    Each rank's RNG is seeded independently (Python's from the OS), so ranks that drew
+    their own seeds would sample different tokens, write their KV shards for different
+    sequences and stop at different steps, and the next collective would hang.  Rank 0
+    of the group draws; the draws are broadcast.  Every rank must call this at the same
+    point (admission is identical on every rank)."""
+    import random
+    seeds = [random.getrandbits(62) for _ in range(n)]
+    if group is None or n == 0:
+        return seeds
+    import torch
+    import torch.distributed as dist
+    dev = device if (device is not None and dist.get_backend(group) == "nccl") else torch.device("cpu")
+    t = torch.tensor(seeds, dtype=torch.int64, device=dev)
+    dist.broadcast(t, src=dist.get_global_rank(group, 0), group=group)
+    return t.tolist()

@@ -98,7 +98,11 @@ class TorchRunner:
         if sp is None or sp.temperature <= 0:
             return None
         g = torch.Generator(device=self.dev)
-        g.manual_seed(sp.seed if sp.seed is not None else int(torch.randint(0, 2**62, (1,))))
+        if sp.seed is not None:
+            g.manual_seed(sp.seed)
+        else:   # one draw shared by the TP ranks (they must sample the same tokens)
+            from .sampling_params import shared_seeds
+            g.manual_seed(shared_seeds(1, self.tp_group, self.dev)[0])
         return dict(sp=sp, gen=g)
 
     def _prefill(self, prompts, rows, params):
