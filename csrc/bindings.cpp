@@ -101,9 +101,6 @@ void mtp_accept(torch::Tensor targets, torch::Tensor tokens, torch::Tensor out_t
 void mtp_finalize(torch::Tensor targets, torch::Tensor n_acc, torch::Tensor drafts, torch::Tensor tokens,
                   torch::Tensor seq_pos, c10::optional<torch::Tensor> active);
 
-void tc_gemm_test(torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch::Tensor sb, torch::Tensor out,
-                  torch::Tensor status, int64_t stage);
-
 void tc_moe_w2(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor> gather, torch::Tensor pairs,
                torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
                torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t nt,
@@ -146,7 +143,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("sorted_tok"), py::arg("pos_of"), py::arg("pairs"), py::arg("n_pairs"), py::arg("counter"),
         py::arg("status"), py::arg("e_lo") = 0, py::arg("E_local") = 0);
   m.def("mla_combine_uv", &mla_combine_uv);
-  m.def("tc_gemm_test", &tc_gemm_test);
   m.def("tc_moe_w2", &tc_moe_w2);
   m.def("tc_gemm_fp8", &tc_gemm_fp8);
   m.def("ws_moe_w2", &ws_moe_w2);

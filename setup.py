@@ -44,7 +44,20 @@ setup(
                                 "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_BFLOAT16_CONVERSIONS__"],
             },
             libraries=["cuda"],
-        )
+        ),
+        # test-only kernels (tests/csrc), a separate module the product never loads
+        CUDAExtension(
+            name="tests.moet_testkit",
+            sources=sorted(glob.glob(os.path.join("tests", "csrc", "*.cpp")) +
+                           glob.glob(os.path.join("tests", "csrc", "*.cu"))),
+            include_dirs=[os.path.join(ROOT, "csrc"), os.path.join(ROOT, "csrc", "kernels")],
+            extra_compile_args={
+                "cxx": ["-O3", "-std=c++17"],
+                "nvcc": ARCH + ["-O3", "-std=c++17", "-lineinfo",
+                                "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_BFLOAT16_CONVERSIONS__"],
+            },
+            libraries=["cuda"],
+        ),
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

@@ -28,7 +28,8 @@ def test_tc_block_scaled_mma_basic(C, N, K):
     sb = torch.randint(122, 132, (N, K // 32), generator=g, dtype=torch.uint8)
     out = torch.zeros(N, 128, device=DEV)
     st = torch.zeros(1, dtype=torch.int32, device=DEV)
-    C.tc_gemm_test(a.view(torch.uint8).to(DEV), sa.to(DEV), b.view(torch.uint8).to(DEV), sb.to(DEV), out, st, 3)
+    import moet_testkit       # test-only extension (tests/csrc)
+    moet_testkit.tc_gemm_test(a.view(torch.uint8).to(DEV), sa.to(DEV), b.view(torch.uint8).to(DEV), sb.to(DEV), out, st, 3)
     A = a.double() * torch.exp2(sa.double() - 127).repeat_interleave(32, 1)
     B = b.double() * torch.exp2(sb.double() - 127).repeat_interleave(32, 1)
     assert int(st) == 0

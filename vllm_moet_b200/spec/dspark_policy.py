@@ -32,7 +32,9 @@ derivation (P:18008-18145); the constants below are that policy's.
 """
 from __future__ import annotations
 
+import math
 import time
+from collections import deque
 from typing import Callable, List, Optional, Sequence, Tuple
 
 import torch
@@ -58,35 +60,44 @@ def accept_curve(survival: Sequence[float], gamma: int) -> List[float]:
 
 
 def bucket_cost(r_grid: Sequence[int], times: Sequence[float], num_reqs: int) -> float:
-    for r, t in zip(r_grid, times):
-        if num_reqs <= r:
-            return float(t)
-    return float(times[-1]) * num_reqs / r_grid[-1]
+    """One table row's step time at `num_reqs` requests (see _step_times)."""
+    return float(_step_times(r_grid, [times], num_reqs)[0])
+
+
+def _step_times(r_grid: Sequence[int], times_by_l: Sequence[Sequence[float]], num_reqs: int) -> torch.Tensor:
+    """Table step time of every L at `num_reqs` requests: column of the first grid bucket
+    holding num_reqs, or the last column scaled by num_reqs / last bucket beyond the grid."""
+    table = torch.as_tensor(times_by_l, dtype=torch.float64)          # [gamma + 1, len(r_grid)]
+    grid = torch.as_tensor(r_grid, dtype=torch.int64)
+    col = int(torch.searchsorted(grid, torch.tensor([num_reqs]), right=False))
+    if col < len(r_grid):
+        return table[:, col]
+    return table[:, -1] * (num_reqs / r_grid[-1])
 
 
 def uniform_length(accept: Sequence[float], num_reqs: int, gamma: int, r_grid: Optional[Sequence[int]],
                    times_by_l: Optional[Sequence[Sequence[float]]], overhead: Tuple[float, float] = (0.0, 0.0),
                    current: Optional[int] = None, hysteresis: float = HYSTERESIS) -> Tuple[int, float]:
     """-> (L maximising tokens / s, that L's predicted step time with overhead).
-    Without a cost table: (gamma, 0)."""
+    Without a cost table: (gamma, 0).  Every L is scored at once: throughput(L) =
+    tokens(L) / (T(R, L) + c0 + c1 tokens(L)); L with a non-positive table time is
+    never chosen; ties go to the shorter L; the incumbent stays unless beaten by more
+    than `hysteresis`."""
     if not r_grid or not times_by_l:
         return gamma, 0.0
     c0, c1 = overhead
-    scored = []
-    for L in range(gamma + 1):
-        t = bucket_cost(r_grid, times_by_l[L], num_reqs)
-        if t <= 0:
-            continue
-        tok = num_reqs * (1.0 + accept[L])
-        t += c0 + c1 * tok
-        scored.append((tok / t, L, t))
-    if not scored:
+    base = _step_times(r_grid, times_by_l, num_reqs)[: gamma + 1]
+    tokens = num_reqs * (1.0 + torch.as_tensor(accept[: gamma + 1], dtype=torch.float64))
+    total = base + c0 + c1 * tokens
+    valid = base > 0
+    if not bool(valid.any()):
         return gamma, 0.0
-    best = max(scored, key=lambda x: (x[0], -x[1]))            # ties: the shorter length
-    inc = next((x for x in scored if x[1] == current), None)
-    if inc is not None and best[0] <= inc[0] * (1.0 + hysteresis):
-        return inc[1], inc[2]
-    return best[1], best[2]
+    rate = torch.where(valid, tokens / total, torch.full_like(total, -math.inf))
+    best = int(torch.argmax(rate))             # argmax returns the first (shortest) maximum
+    if current is not None and 0 <= current <= gamma and bool(valid[current]):
+        if float(rate[best]) <= float(rate[current]) * (1.0 + hysteresis):
+            best = current
+    return best, float(total[best])
 
 
 def derive_schedule(r_grid: Sequence[int], times_by_l: Sequence[Sequence[float]], survival: Sequence[float],
@@ -159,7 +170,8 @@ class DSparkPolicy:
         self.r_grid: Optional[List[int]] = None
         self.times_by_l: Optional[List[List[float]]] = None
         self.c0 = self.c1 = 0.0
-        self.samples: List[Tuple[float, float]] = []
+        self.samples: "deque[Tuple[float, float]]" = deque()
+        self._sums = [0.0, 0.0, 0.0, 0.0]        # running sums of x, y, x*x, x*y over `samples`
         self.ema: Optional[torch.Tensor] = None
         self.cal = torch.ones(gamma)
         self.acc = torch.zeros(gamma)
@@ -179,21 +191,29 @@ class DSparkPolicy:
 
     # -------------------------------------------------------------- overhead regression
     def _observe_overhead(self, now: float) -> None:
+        """Fit the engine overhead o = c0 + c1 * tokens to the last RING steps.  Running
+        sums of x, y, x^2 and xy over the ring are updated as samples enter and leave, so
+        each step costs O(1); the fit is the closed-form least-squares line through them."""
         if self._t_last is not None and self._gpu_pred > 0:
             o = (now - self._t_last) - self._gpu_pred
             if 0.0 <= o < GATE_S:
-                self.samples.append((self._tokens, o))
-                del self.samples[:-RING]
-                if len(self.samples) >= MIN_SAMPLES:
-                    n = len(self.samples)
-                    mx = sum(x for x, _ in self.samples) / n
-                    my = sum(y for _, y in self.samples) / n
-                    var = sum((x - mx) ** 2 for x, _ in self.samples)
-                    if var > 1e-6:
-                        cov = sum((x - mx) * (y - my) for x, y in self.samples)
-                        self.c1 = min(max(cov / var, 0.0), C1_MAX)
-                    self.c0 = max(my - self.c1 * mx, 0.0)
+                self._fit_add(self._tokens, o)
+                n = len(self.samples)
+                if n >= MIN_SAMPLES:
+                    sx, sy, sxx, sxy = self._sums
+                    sxx_c = sxx - sx * sx / n           # sum of squared deviations of x
+                    if sxx_c > 1e-6:
+                        slope = (sxy - sx * sy / n) / sxx_c
+                        self.c1 = min(max(slope, 0.0), C1_MAX)
+                    self.c0 = max(sy / n - self.c1 * sx / n, 0.0)
         self._t_last = now
+
+    def _fit_add(self, x: float, y: float) -> None:
+        if len(self.samples) == RING:
+            ox, oy = self.samples.popleft()
+            self._sums = [a - b for a, b in zip(self._sums, (ox, oy, ox * ox, ox * oy))]
+        self.samples.append((x, y))
+        self._sums = [a + b for a, b in zip(self._sums, (x, y, x * x, x * y))]
 
     def survival_curve(self) -> Optional[List[float]]:
         if self.ema is None:
