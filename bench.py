@@ -9,8 +9,9 @@ tok/s reported alongside.  `value` is device-timed: K decode steps replayed
 back to back from the captured graph (each step is a full MTP verify +
 draft step that advances the sequence on the device), between a barrier +
 synchronize on both sides, max over ranks.  `e2e` is the same metric
-through the public `LLM.generate` API, which per step copies the row-activity
-vector H2D from pinned memory and reads emitted tokens D2H.  Each decode
+through the public `LLM.generate` API, timed on the host from the first emitted
+token to completion: per step it copies the row-activity vector H2D from pinned
+memory, replays the graph, reads the emitted tokens D2H and runs the host loop.  Each decode
 step streams ~7 GB of weights (>> 126 MB L2), so no L2 flush is needed.
 """
 from __future__ import annotations
@@ -98,28 +99,29 @@ def main():
     st.block_table.copy_(bt)
     runner.prefill([prompt(args.prompt_len)], [bt[0].tolist()], [0], st)
     st.set_active(torch.ones(1, dtype=torch.int32, device="cuda"))
-    runner.decode_body_eager_warm(st)
-    counter = LaunchCounter(runner.C)     # counts the native launches recorded into the graph
+    # count the native launches of one step on the eager warm-up pass (the same code path the
+    # graph records), then capture with the plain module
+    counter = LaunchCounter(runner.C)
     real_C = runner.C
     runner.C = counter
-    graph = runner.capture(st, warm=False)
+    try:
+        runner.decode_body_eager_warm(st)
+    finally:
+        runner.C = real_C
     launches_per_step = counter.count
-    runner.C = real_C
-    accepted0 = 0
+    graph = runner.capture(st, warm=False)
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize()
-    acc_before = None
+    pos0 = int(st.seq_pos[0])
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n_acc_sum = torch.zeros(1, dtype=torch.int64, device="cuda")
     with ClockSampler(local) as clk:
         s_ev.record()
-        for _ in range(args.steps):
+        for _ in range(args.steps):       # nothing but graph replays between the events
             graph.replay()
-            n_acc_sum += st.n_acc.sum()
         e_ev.record()
         torch.cuda.synchronize()
     if world > 1:
@@ -129,17 +131,21 @@ def main():
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t)
-    acc = float(n_acc_sum) / args.steps
+    # every step advances the sequence by 1 + accepted drafts
+    acc = (int(st.seq_pos[0]) - pos0) / args.steps - 1.0
     tok_per_step = 1.0 + acc
     value = tok_per_step * 1000.0 / ms
     llm.blocks.release("bench")
 
     # ---- e2e through LLM.generate (1 stream) -----------------------------------------------
+    # host wall clock from the first emitted token to the request's completion: every decode
+    # step's H2D copy of the row-activity vector from pinned memory, graph replay, D2H read of
+    # the emitted tokens and all host work between steps (emit, stop checks, detokenise)
     n_tok = args.steps + 1
     llm.generate([prompt(args.prompt_len)], SamplingParams(max_tokens=4, ignore_eos=True))  # warm
     outs = llm.generate([prompt(args.prompt_len)], SamplingParams(max_tokens=n_tok, ignore_eos=True))
-    st_e2e = dict(llm.stats)
-    e2e_tok_s = (len(outs[0].outputs[0].token_ids) - 1) / maxr(st_e2e["decode_s"])
+    m = outs[0].metrics
+    e2e_tok_s = (len(outs[0].outputs[0].token_ids) - 1) / maxr(m["e2e_s"] - m["ttft_s"])
 
     extra, errors = {}, {}
 
@@ -160,7 +166,10 @@ def main():
                             SamplingParams(max_tokens=args.steps + 1, ignore_eos=True))
         stt = dict(llm.stats)
         gen = sum(len(o.outputs[0].token_ids) - 1 for o in outs)
-        dec_s = maxr(stt["decode_s"])
+        # wall clock from the first emitted token to the last request's completion
+        first = min(o.metrics["ttft_s"] for o in outs)
+        last = max(o.metrics["e2e_s"] for o in outs)
+        dec_s = maxr(last - first)
         extra[f"decode_{S}_streams_tok_s"] = gen / dec_s
         extra[f"decode_{S}_streams_steps_s"] = stt["steps"] / dec_s
 

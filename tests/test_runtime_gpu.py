@@ -27,6 +27,17 @@ def _prompt(n, seed):
     return torch.randint(3, 2048, (n,), generator=g).tolist()
 
 
+def _rel(a, b):
+    return float((a - b).norm() / b.norm())
+
+
+def _oracle_last_logits(llm, prompt):
+    cs = reference.rope_cos_sin(llm.cfg, len(prompt) + 64, "cuda")
+    t = torch.tensor(prompt, device="cuda")
+    lg, _ = reference.forward(llm.mw, t, torch.arange(len(prompt), device="cuda"), cs)
+    return lg[-1]
+
+
 def test_prefill_logits_match_reference(llm):
     p = _prompt(70, 0)
     runner = llm.runner
@@ -204,9 +215,12 @@ def test_prefix_cached_prefill_matches_full_prefill():
     full = LLM(small_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=1024, max_num_seqs=4)
     want = full.generate([b], sp)[0].outputs[0].token_ids
     lg_full = full.runner.ws_prefill.bufs[("main.logits", torch.float32)][: full.cfg.vocab].clone()
-    rel = float((lg_cached - lg_full).norm() / lg_full.norm())
-    assert rel < 0.05, rel
-    assert got[0] == want[0] or float(lg_full[got[0]]) >= float(lg_full.max()) - 0.3
+    # both native paths against the fp32 oracle: the cached (absorbed-attention) prefill is
+    # within the full prefill's own tolerance and not materially worse than it
+    r = _oracle_last_logits(pc, b)
+    e_cached, e_full = _rel(lg_cached, r), _rel(lg_full, r)
+    assert e_cached < 0.08 and e_cached <= e_full + 0.03, (e_cached, e_full)
+    assert got[0] == want[0] or float(r[got[0]]) >= float(r.max()) - 0.3
 
 
 def test_chunked_prefill_matches_full_prefill():
@@ -222,5 +236,6 @@ def test_chunked_prefill_matches_full_prefill():
     full = LLM(small_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=1024, max_num_seqs=4)
     full.generate([p], sp)
     lg_full = full.runner.ws_prefill.bufs[("main.logits", torch.float32)][: full.cfg.vocab].clone()
-    rel = float((lg_chunked - lg_full).norm() / lg_full.norm())
-    assert rel < 0.05, rel
+    r = _oracle_last_logits(ch, p)
+    e_chunked, e_full = _rel(lg_chunked, r), _rel(lg_full, r)
+    assert e_chunked < 0.08 and e_chunked <= e_full + 0.03, (e_chunked, e_full)
