@@ -219,7 +219,7 @@ def test_prefix_cached_prefill_matches_full_prefill():
     # within the full prefill's own tolerance and not materially worse than it
     r = _oracle_last_logits(pc, b)
     e_cached, e_full = _rel(lg_cached, r), _rel(lg_full, r)
-    assert e_cached < 0.08 and e_cached <= e_full + 0.03, (e_cached, e_full)
+    assert e_cached < 0.1 and e_cached <= e_full + 0.02, (e_cached, e_full)
     assert got[0] == want[0] or float(r[got[0]]) >= float(r.max()) - 0.3
 
 
