@@ -34,6 +34,7 @@ void argmax_split(torch::Tensor logits, c10::optional<torch::Tensor> ids, c10::o
                   c10::optional<torch::Tensor> status, torch::Tensor part, torch::Tensor counter,
                   c10::optional<torch::Tensor> mv, int64_t id_offset);
 void argmax_merge(torch::Tensor parts, torch::Tensor ids);
+void argmax_merge_ar(torch::Tensor mv, torch::Tensor ids, torch::Tensor ar);
 void build_pairs_padded(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor rank_scratch,
                         torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
                         torch::Tensor n_rows, torch::Tensor status, int64_t e_lo);
@@ -45,6 +46,14 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
                  torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
                  c10::optional<torch::Tensor> miss_count, c10::optional<torch::Tensor> pool8, int64_t codes_off8,
                  int64_t scale_off8, c10::optional<torch::Tensor> slot_table8, bool quintal);
+void moe_w2_gemv_split(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor> gather, torch::Tensor pairs,
+                       torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
+                       torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
+                       c10::optional<torch::Tensor> miss_count);
+void moe_w2_tcd(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor> gather, torch::Tensor pairs,
+                torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
+                torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
+                c10::optional<torch::Tensor> miss_count, torch::Tensor status);
 void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::optional<torch::Tensor> resid,
                  c10::optional<torch::Tensor> shared_out, c10::optional<torch::Tensor> out,
                  c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> ar);
@@ -52,7 +61,8 @@ void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::
 void gemv_stream_fp8(c10::optional<torch::Tensor> a, c10::optional<torch::Tensor> sa, torch::Tensor w,
                      torch::Tensor sw, torch::Tensor out, c10::optional<torch::Tensor> resid, torch::Tensor status,
                      c10::optional<torch::Tensor> x_norm, c10::optional<torch::Tensor> gamma, double eps,
-                     c10::optional<torch::Tensor> x_add, c10::optional<torch::Tensor> x_out);
+                     c10::optional<torch::Tensor> x_add, c10::optional<torch::Tensor> x_out,
+                     c10::optional<torch::Tensor> ar_push, c10::optional<torch::Tensor> ar_consume);
 // indexer.cu
 void indexer_logits(torch::Tensor q, torch::Tensor w, torch::Tensor k_cache, torch::Tensor block_table,
                     torch::Tensor seq_of_tok, torch::Tensor pos_of_tok, torch::Tensor out, torch::Tensor status);
@@ -150,11 +160,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax_split", &argmax_split, py::arg("logits"), py::arg("ids"), py::arg("lse"), py::arg("status"),
         py::arg("part"), py::arg("counter"), py::arg("mv") = py::none(), py::arg("id_offset") = 0);
   m.def("argmax_merge", &argmax_merge);
+  m.def("argmax_merge_ar", &argmax_merge_ar);
   m.def("moe_w2_gemv", &moe_w2_gemv, py::arg("a"), py::arg("sa"), py::arg("gather"), py::arg("pairs"),
         py::arg("n_pairs"), py::arg("pool"), py::arg("codes_off"), py::arg("scale_off"), py::arg("slot_table"),
         py::arg("out"), py::arg("N"), py::arg("K"), py::arg("rows_per_pair"), py::arg("miss_count"),
         py::arg("pool8") = py::none(), py::arg("codes_off8") = 0, py::arg("scale_off8") = 0,
         py::arg("slot_table8") = py::none(), py::arg("quintal") = false);
+  m.def("moe_w2_gemv_split", &moe_w2_gemv_split);
+  m.def("moe_w2_tcd", &moe_w2_tcd);
   m.def("moe_combine", &moe_combine, py::arg("y"), py::arg("pos_of"), py::arg("wts"), py::arg("resid"),
         py::arg("shared_out"), py::arg("out"), py::arg("out_f32"), py::arg("ar") = py::none());
   m.def("bf12_decode", &bf12_decode);
@@ -162,7 +175,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("indexer_topk", &indexer_topk);
   m.def("gemv_stream_fp8", &gemv_stream_fp8, py::arg("a"), py::arg("sa"), py::arg("w"), py::arg("sw"), py::arg("out"),
         py::arg("resid"), py::arg("status"), py::arg("x_norm") = py::none(), py::arg("gamma") = py::none(),
-        py::arg("eps") = 1e-6, py::arg("x_add") = py::none(), py::arg("x_out") = py::none());
+        py::arg("eps") = 1e-6, py::arg("x_add") = py::none(), py::arg("x_out") = py::none(),
+        py::arg("ar_push") = py::none(), py::arg("ar_consume") = py::none());
   m.def("idx_k_write", &idx_k_write);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);

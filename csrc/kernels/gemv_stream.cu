@@ -14,6 +14,7 @@
 // activation scales per 64-k chunk, and the warps' partial sums are reduced
 // through shared memory before the next block.  All waits are bounded.
 #include "common.cuh"
+#include "symm.cuh"
 #include "torch_glue.h"
 
 namespace moet {
@@ -59,13 +60,33 @@ struct GemvStreamArgs {
   const __nv_bfloat16* xin; long long xin_stride; const __nv_bfloat16* gamma; float eps;
   // optional residual add before the norm: x = bf16(xin + xadd), written to xout by CTA 0
   const __nv_bfloat16* xadd; __nv_bfloat16* xout; long long xadd_stride;
+  // fused TP all-reduce: push the output instead of storing it / consume into the norm input
+  int ar_push, ar_consume;
+  ArDesc ar;
 };
 
-// 8 bf16 of row r at column c of (xin [+ xadd]), the sum rounded to bf16 as the residual stream stores it
-MOET_DEVICE void gs_load8(const GemvStreamArgs& p, int r, int c, float (&v)[8]) {
+// 8 bf16 of row r at column c of (xin [+ xadd | + all-reduced partials]), the sum rounded to
+// bf16 as the residual stream stores it
+MOET_DEVICE void gs_load8(const GemvStreamArgs& p, int r, int c, float (&v)[8], unsigned long long epoch) {
   const uint4 a = *reinterpret_cast<const uint4*>(p.xin + (size_t)r * p.xin_stride + c);
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&a);
-  if (p.xadd) {
+  if (p.ar_consume) {
+    float s[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) s[q] = 0.f;
+    for (int w = 0; w < p.ar.world; w++) {
+      const float4* src = reinterpret_cast<const float4*>(ar_slot(p.ar, p.ar.rank, epoch, w) + (size_t)r * p.K + c);
+      const float4 f0 = src[0], f1 = src[1];
+      s[0] += f0.x; s[1] += f0.y; s[2] += f0.z; s[3] += f0.w;
+      s[4] += f1.x; s[5] += f1.y; s[6] += f1.z; s[7] += f1.w;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const float2 f = __bfloat1622float2(h[q]);
+      v[2 * q] = __bfloat162float(__float2bfloat16(f.x + s[2 * q]));
+      v[2 * q + 1] = __bfloat162float(__float2bfloat16(f.y + s[2 * q + 1]));
+    }
+  } else if (p.xadd) {
     const uint4 b = *reinterpret_cast<const uint4*>(p.xadd + (size_t)r * p.xadd_stride + c);
     const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&b);
 #pragma unroll
@@ -112,6 +133,15 @@ __global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStr
     for (int i = 0; i < min(kRing, nmine); i++) issue(i);
   pdl_entry();
   const int ng = p.K / 64;
+  const unsigned long long epoch = (p.ar_push || p.ar_consume) ? ar_epoch(p.ar) : 0ull;
+  if (p.ar_consume && !ar_consumer_wait(p.ar, epoch)) {
+    ar_consumer_done(p.ar);
+    // timed out (status records kTimeout): drain the weight copies already in flight, then leave
+    if (threadIdx.x == 0)
+      for (int i = 0; i < min(kRing, nmine); i++) bar_wait(&bars[i], 0u);
+    __syncthreads();
+    return;
+  }
   if (p.xin == nullptr) {
     // activations (zero rows beyond T) -> shared memory
     for (int i = threadIdx.x; i < kMaxT * (p.K / 16); i += blockDim.x) {
@@ -134,7 +164,7 @@ __global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStr
 #pragma unroll
       for (int u = 0; u < 8; u++) {
         float v[8];
-        gs_load8(p, r, c * 64 + u * 8, v);
+        gs_load8(p, r, c * 64 + u * 8, v, epoch);
 #pragma unroll
         for (int q = 0; q < 8; q++) acc = fmaf(v[q], v[q], acc);
       }
@@ -158,7 +188,7 @@ __global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStr
 #pragma unroll
       for (int u = 0; u < 8; u++) {
         float v[8];
-        gs_load8(p, r, c * 64 + u * 8, v);
+        gs_load8(p, r, c * 64 + u * 8, v, epoch);
         if (p.xout && blockIdx.x == 0) {    // the summed residual stream, written once
           uint32_t o[4];
 #pragma unroll
@@ -192,6 +222,7 @@ __global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStr
     }
   }
   __syncthreads();
+  if (p.ar_consume) ar_consumer_done(p.ar);   // the receive slots are no longer read
   const int nchunks = p.K / 64;
   const int cpw = (nchunks + kWarps - 1) / kWarps;          // 64-k chunks per warp
   const int c_lo = warp * cpw, c_hi = min(nchunks, c_lo + cpw);
@@ -241,12 +272,18 @@ __global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStr
       float v = 0.f;
 #pragma unroll
       for (int w = 0; w < kWarps; w++) v += rr[(size_t)w * kRows * kMaxT + o];
+      if (p.ar_push) {      // row-parallel partial -> slot [rank] of every peer
+        const size_t aoff = (size_t)tok * p.N + r0 + row;
+        for (int q = 0; q < p.ar.world; q++) ar_slot(p.ar, q, epoch, p.ar.rank)[aoff] = v;
+        continue;
+      }
       const size_t off = (size_t)tok * p.out_stride + r0 + row;
       if (p.resid) v += __bfloat162float(p.resid[off]);
       if (p.out_f32) reinterpret_cast<float*>(p.out)[off] = v;
       else reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16(v);
     }
   }
+  if (p.ar_push) ar_producer_arrive(p.ar, epoch);
 }
 
 }  // namespace moet
@@ -257,7 +294,8 @@ using namespace moet;
 void gemv_stream_fp8(c10::optional<torch::Tensor> a_opt, c10::optional<torch::Tensor> sa_opt, torch::Tensor w,
                      torch::Tensor sw, torch::Tensor out, c10::optional<torch::Tensor> resid, torch::Tensor status,
                      c10::optional<torch::Tensor> x_norm, c10::optional<torch::Tensor> gamma, double eps,
-                     c10::optional<torch::Tensor> x_add, c10::optional<torch::Tensor> x_out) {
+                     c10::optional<torch::Tensor> x_add, c10::optional<torch::Tensor> x_out,
+                     c10::optional<torch::Tensor> ar_push, c10::optional<torch::Tensor> ar_consume) {
   const bool fuse = x_norm.has_value() && x_norm->defined();
   const torch::Tensor& a = fuse ? *x_norm : *a_opt;
   const int T = a.size(0), K = w.size(1), N = w.size(0);
@@ -286,6 +324,21 @@ void gemv_stream_fp8(c10::optional<torch::Tensor> a_opt, c10::optional<torch::Te
     TORCH_CHECK(x_add->scalar_type() == at::kBFloat16 && x_add->stride(1) == 1 && x_add->size(1) == K &&
                 x_out.has_value() && x_out->is_contiguous() && x_out->size(1) == K, "gemv_stream_fp8: x_add / x_out");
     p.xadd = (const __nv_bfloat16*)x_add->data_ptr(); p.xadd_stride = x_add->stride(0);
+    p.xout = (__nv_bfloat16*)x_out->data_ptr();
+  }
+  p.ar_push = ar_push.has_value() && ar_push->defined();
+  p.ar_consume = ar_consume.has_value() && ar_consume->defined();
+  p.ar = ArDesc{};
+  if (p.ar_push) {
+    p.ar = ar_desc_from(*ar_push);
+    TORCH_CHECK((int64_t)T * N <= p.ar.cap, "gemv_stream_fp8: T*N exceeds the all-reduce slot");
+  }
+  if (p.ar_consume) {
+    TORCH_CHECK(fuse && !p.xadd && x_out.has_value() && x_out->is_contiguous() && x_out->size(1) == K &&
+                a.stride(0) == K && !p.ar_push, "gemv_stream_fp8: all-reduce consumer needs the fused norm, "
+                "a contiguous residual and x_out");
+    p.ar = ar_desc_from(*ar_consume);
+    TORCH_CHECK((int64_t)T * K <= p.ar.cap, "gemv_stream_fp8: T*K exceeds the all-reduce slot");
     p.xout = (__nv_bfloat16*)x_out->data_ptr();
   }
   p.W = (const uint8_t*)w.data_ptr(); p.sW = (const uint8_t*)sw.data_ptr(); p.sw_cols = sw.size(1);

@@ -138,7 +138,8 @@ __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x_in,
 // the product is rounded to bf16 before quantisation (matches a bf16 module).
 __global__ void swiglu_quant_kernel(const float* __restrict__ in, int I, float limit,
                                     const int* __restrict__ n_rows, int layout,
-                                    uint8_t* __restrict__ q, uint8_t* __restrict__ s) {
+                                    uint8_t* __restrict__ q, uint8_t* __restrict__ s,
+                                    int nsplit, long long split_stride) {
   pdl_entry();
   const int row = blockIdx.x;
   if (n_rows && row >= *n_rows) return;
@@ -150,6 +151,10 @@ __global__ void swiglu_quant_kernel(const float* __restrict__ in, int I, float l
 #pragma unroll
     for (int i = 0; i < VEC; i++) {
       float gv = g[i], uv = u[i];
+      for (int q = 1; q < nsplit; q++) {   // K-slice partials of the expert GEMV, slice order
+        gv += g[q * split_stride + i];
+        uv += u[q * split_stride + i];
+      }
       if (limit > 0.f) { gv = fminf(gv, limit); uv = fminf(fmaxf(uv, -limit), limit); }
       float a = gv / (1.f + __expf(-gv)) * uv;
       v[i] = __bfloat162float(__float2bfloat16(a));
@@ -212,15 +217,19 @@ void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> add, c10::optio
 
 void swiglu_quant(torch::Tensor in, double limit, c10::optional<torch::Tensor> n_rows, int64_t layout,
                   torch::Tensor q, torch::Tensor s) {
+  // in: [rows, 2I] or [nsplit, rows, 2I] (K-slice partials, summed in slice order)
   TORCH_CHECK(in.scalar_type() == at::kFloat && in.is_contiguous(), "in must be contiguous f32");
-  const int rows = in.size(0), I = in.size(1) / 2;
+  const int nsplit = in.dim() == 3 ? in.size(0) : 1;
+  const long long split_stride = in.dim() == 3 ? in.stride(0) : 0;
+  const int rows = in.size(-2), I = in.size(-1) / 2;
   TORCH_CHECK(I % 64 == 0, "I must be a multiple of 64");
   if (rows == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   int threads = std::min(256, I / 8);
   launch_k(swiglu_quant_kernel, rows, threads, 0, stream, in.data_ptr<float>(), I, (float)limit,
                                                     (const int*)opt_ptr(n_rows), (int)layout,
-                                                    (uint8_t*)q.data_ptr(), (uint8_t*)s.data_ptr());
+                                                    (uint8_t*)q.data_ptr(), (uint8_t*)s.data_ptr(),
+                                                    nsplit, split_stride);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

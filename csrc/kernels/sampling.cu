@@ -8,6 +8,7 @@
 //   mtp_finalize: advances the per-sequence position and builds the next step's
 //                 input tokens [target[a], draft_1 .. draft_k].
 #include "common.cuh"
+#include "symm.cuh"
 #include "torch_glue.h"
 
 namespace moet {
@@ -179,9 +180,47 @@ __global__ void argmax_merge_kernel(const float2* __restrict__ parts, int W, int
   ids[r] = I == 0x7fffffff ? 0 : I;
 }
 
+// Vocab-parallel argmax merge over peer memory (replaces an all-gather + merge): one CTA
+// pushes this rank's (max, id) pairs [R] into slot [rank] of every peer's receive area and
+// publishes the epoch; it then waits (bounded) for the W ranks and merges their pairs in
+// rank order, ties to the smaller id.  Every rank computes the same ids.
+__global__ void argmax_merge_ar_kernel(const float2* __restrict__ mine, int R, int* __restrict__ ids, ArDesc ar) {
+  pdl_entry();
+  const unsigned long long epoch = ar_epoch(ar);
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    const float2 v = mine[r];
+    for (int q = 0; q < ar.world; q++) reinterpret_cast<float2*>(ar_slot(ar, q, epoch, ar.rank))[r] = v;
+  }
+  ar_producer_arrive(ar, epoch);
+  const bool ok = ar_consumer_wait(ar, epoch);
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    float M = -INFINITY; int I = 0x7fffffff;
+    if (ok)
+      for (int w = 0; w < ar.world; w++) {
+        const float2 p = reinterpret_cast<const float2*>(ar_slot(ar, ar.rank, epoch, w))[r];
+        const int id = __float_as_int(p.y);
+        if (p.x > M || (p.x == M && id < I)) { M = p.x; I = id; }
+      }
+    ids[r] = I == 0x7fffffff ? 0 : I;
+  }
+  ar_consumer_done(ar);
+}
+
 }  // namespace moet
 
 using namespace moet;
+
+void argmax_merge_ar(torch::Tensor mv, torch::Tensor ids, torch::Tensor ar) {
+  TORCH_CHECK(mv.scalar_type() == at::kFloat && mv.dim() == 2 && mv.size(1) == 2 && mv.is_contiguous(),
+              "argmax_merge_ar: mv [R, 2] f32");
+  const int R = mv.size(0);
+  ArDesc d = ar_desc_from(ar);
+  TORCH_CHECK(ids.numel() >= R && 2LL * R <= d.cap, "argmax_merge_ar: ids / slot size");
+  if (R == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  launch_k(argmax_merge_ar_kernel, 1, 256, 0, stream, (const float2*)mv.data_ptr(), R, ids.data_ptr<int>(), d);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 
 void argmax_split(torch::Tensor logits, c10::optional<torch::Tensor> ids, c10::optional<torch::Tensor> lse,
                   c10::optional<torch::Tensor> status, torch::Tensor part, torch::Tensor counter,

@@ -193,6 +193,83 @@ def test_moe_w2_scale_folding_wide_exponent_range(C):
             assert rel(out[int(posof[t * 2 + j])].cpu(), A[t] @ W.t()) < 1e-4
 
 
+@pytest.mark.parametrize("impl", ["split", "tcd"])
+@pytest.mark.parametrize("T,k,E,N,K,MB,ks,lo,hi", [(1, 8, 16, 64, 256, 8, 2, 122, 130),
+                                                   (3, 8, 16, 128, 4096, 8, 8, 100, 130),
+                                                   (40, 4, 8, 64, 192, 16, 3, 122, 130),
+                                                   (96, 8, 32, 64, 1536, 32, 3, 110, 119),
+                                                   (2, 8, 16, 32, 512, 8, 1, 60, 131),
+                                                   (20, 4, 8, 208, 384, 16, 3, 118, 132),
+                                                   (3, 8, 16, 64, 1536, 8, 5, 120, 132)])
+def test_moe_w2_gemv_split(C, impl, T, k, E, N, K, MB, ks, lo, hi):
+    """The K-sliced decode expert GEMVs -- mma.sync with the block scales folded into the
+    lookup words ("split"), and the tcgen05 block-scaled MMA ("tcd") -- summed over their
+    slices in order equal the fp64 dequantised reference, including scale ranges wide
+    enough to need subnormal / flushed levels in the folded form, partial 128-row tiles
+    and slices past the end of K; a missing expert gives zero rows and a miss count.  The
+    split-aware consumers (swiglu_quant, moe_combine) equal their one-slice results on the
+    summed tensor."""
+    if impl == "tcd" and (K % 128 or MB not in (8, 16)):
+        pytest.skip("tcgen05 decode kernel: K % 128 == 0, 8 or 16 rows per pair")
+    if impl == "split" and -(-(K // 64) // ks) > 8:
+        pytest.skip("mma.sync split kernel: at most 8 chunks per slice")
+    g = torch.Generator().manual_seed(T * 131 + K)
+    codes, sc, pool = _expert_pool(E, N, K, g, lo=lo, hi=hi)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).int()
+    R = T * k
+    P = R // MB + min(E, R)
+    dev = lambda t: t.to(DEV)  # noqa: E731
+    rank, stok, posof = (torch.empty(R, dtype=torch.int32, device=DEV) for _ in range(3))
+    pairs = torch.empty(P, 4, dtype=torch.int32, device=DEV); npairs = torch.zeros(1, dtype=torch.int32, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    C.build_pairs(dev(ids), E, MB, rank, stok, posof, pairs, npairs, status)
+    x = torch.randn(T, K, generator=g)
+    q, s = fp8.quant_act_fp8(x)
+    qw2 = dev(fp8.to_w2_layout(q.view(torch.uint8)))
+    out = torch.full((ks, R, N), float("nan"), device=DEV)
+    slot_table = torch.arange(E, dtype=torch.int32, device=DEV)
+    miss = torch.zeros(1, dtype=torch.int32, device=DEV)
+    def run():
+        if impl == "tcd":
+            C.moe_w2_tcd(qw2, dev(s), stok, pairs, npairs, dev(pool), 0, N * K // 4, slot_table, out, N, K, MB, miss,
+                         status)
+        else:
+            C.moe_w2_gemv_split(qw2, dev(s), stok, pairs, npairs, dev(pool), 0, N * K // 4, slot_table, out, N, K,
+                                MB, miss)
+    run()
+    tot = out.sum(0).cpu().double()
+    A = fp8.dequant_act_fp8(q, s).double()
+    posof_c = posof.cpu().long()
+    for t in range(T):
+        for j in range(k):
+            e = int(ids[t, j])
+            W = codebook.dequant_codes(codes[e], sc[e]).double()
+            ref = A[t] @ W.t()
+            # levels 2^-10 below a group's block maximum flush: bounded by the largest term
+            tol = 1e-4 if (hi - lo < 16 or impl == "tcd") else 2e-3
+            assert rel(tot[posof_c[t * k + j]], ref) < tol, (t, j)
+    assert int(miss) == 0 and int(status) == 0
+    # split-aware consumers
+    if N % 128 == 0:
+        I = N // 2
+        qa = torch.empty(R, I, dtype=torch.uint8, device=DEV); sa = torch.empty(R, I // 64, dtype=torch.uint8, device=DEV)
+        qb = torch.empty_like(qa); sb = torch.empty_like(sa)
+        C.swiglu_quant(out, 0.0, None, 1, qa, sa)
+        C.swiglu_quant(out.sum(0).contiguous(), 0.0, None, 1, qb, sb)
+        assert (qa.view(torch.float8_e4m3fn).float() - qb.view(torch.float8_e4m3fn).float()).abs().max() <= 0.5 * \
+            qb.view(torch.float8_e4m3fn).float().abs().max() * 2 ** -3
+    w = torch.rand(T, k, generator=g).to(DEV)
+    o1 = torch.empty(T, N, dtype=torch.bfloat16, device=DEV); o2 = torch.empty_like(o1)
+    C.moe_combine(out, posof, w, None, None, o1, None)
+    C.moe_combine(out.sum(0).contiguous(), posof, w, None, None, o2, None)
+    assert rel(o1.float().cpu(), o2.float().cpu()) < 1e-2
+    # a missing expert writes zeros in every slice and counts a miss
+    slot_table[int(ids[0, 0])] = -1
+    run()
+    assert int(miss) >= 1 and int(status) == 0
+    assert (out[:, posof_c[0]] == 0).all()
+
+
 def test_moe_combine(C):
     g = torch.Generator().manual_seed(3)
     T, k, H = 5, 4, 256

@@ -37,6 +37,58 @@ def test_symm_allreduce_loopback_and_timeout():
     ar.close()
 
 
+@pytest.mark.parametrize("T,H,N", [(3, 4096, 1600), (8, 1024, 512), (1, 2048, 4096)])
+def test_gemv_stream_allreduce_push_consume_loopback(T, H, N):
+    """World-1 loopback of the fused TP reduction in the streaming GEMV: a row-parallel
+    GEMV pushes its fp32 partial, the next GEMV's norm prologue consumes it.  The new
+    residual stream and the consumer's output equal the unfused sequence (fp32 partial,
+    bf16 residual add, fused-norm GEMV) bit for bit."""
+    from vllm_moet_b200.formats import fp8
+    from vllm_moet_b200.models.weights import Fp8Linear
+    from vllm_moet_b200.parallel.symm import SymmAllReduce
+    C = _C()
+    g = torch.Generator().manual_seed(T * H + N)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ar = SymmAllReduce(None, 128 * H, "cuda", status, spin_limit=1 << 20)
+    Ko = 1024                                   # producer (o_proj-like) K
+    lo = Fp8Linear.from_float(torch.randn(H, Ko, generator=g) * 0.05)
+    lq = Fp8Linear.from_float(torch.randn(N, H, generator=g) * 0.05)
+    aq, sa = fp8.quant_act_fp8(torch.randn(T, Ko, generator=g))
+    aq, sa = aq.view(torch.uint8).cuda(), sa.cuda()
+    resid = (torch.randn(T, H, generator=g)).to(torch.bfloat16).cuda()
+    gamma = (torch.rand(H, generator=g) + 0.5).to(torch.bfloat16).cuda()
+    # unfused reference
+    part = torch.empty(T, H, device="cuda")
+    C.gemv_stream_fp8(aq, sa, lo.w.cuda(), lo.s.cuda(), part, None, status)
+    xnew = (resid.float() + part).to(torch.bfloat16)
+    want = torch.empty(T, N, device="cuda")
+    C.gemv_stream_fp8(None, None, lq.w.cuda(), lq.s.cuda(), want, None, status, xnew, gamma, 1e-6)
+    for _ in range(3):      # alternating parities
+        xout = torch.zeros(T, H, dtype=torch.bfloat16, device="cuda")
+        got = torch.empty(T, N, device="cuda")
+        dummy = torch.empty(T, H, device="cuda")
+        C.gemv_stream_fp8(aq, sa, lo.w.cuda(), lo.s.cuda(), dummy, None, status, ar_push=ar.desc)
+        C.gemv_stream_fp8(None, None, lq.w.cuda(), lq.s.cuda(), got, None, status, resid, gamma, 1e-6,
+                          None, xout, None, ar.desc)
+        torch.cuda.synchronize()
+        assert int(status) == 0
+        assert torch.equal(xout, xnew)
+        assert torch.equal(got, want)
+    # argmax merge over the same buffers (world 1: the local pairs)
+    mv = torch.tensor([[1.5, 7.0], [-2.0, 3.0]], device="cuda")
+    mv[:, 1] = torch.tensor([7, 3], dtype=torch.int32, device="cuda").view(torch.float32)
+    ids = torch.zeros(2, dtype=torch.int32, device="cuda")
+    C.argmax_merge_ar(mv, ids, ar.desc)
+    torch.cuda.synchronize()
+    assert ids.tolist() == [7, 3] and int(status) == 0
+    # a consumer whose producer never ran times out (kTimeout = 2) and leaves the GPU usable
+    C.gemv_stream_fp8(None, None, lq.w.cuda(), lq.s.cuda(), got, None, status, resid, gamma, 1e-6,
+                      None, xout, None, ar.desc)
+    torch.cuda.synchronize()
+    assert int(status) == 2
+    ar.close()
+
+
 def _small_cfg():
     from vllm_moet_b200.config import ds4_flash_config
     return ds4_flash_config(num_layers=3, hidden=1024, vocab=2048, num_experts=16, moe_intermediate=256,

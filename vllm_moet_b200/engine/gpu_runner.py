@@ -138,6 +138,10 @@ class NativeRunner:
         self.mb8_max_r = int(os.environ.get("MOET_MB8_MAX_R", "2048"))
         # decode experts on the tcgen05 kernel with this token tile (0: mma.sync GEMV)
         self.decode_tc_nt = int(os.environ.get("MOET_DECODE_TC_NT", "0"))
+        # decode experts over the 2-bit base: "tcd" (tcgen05, K-sliced), "split" (mma.sync, K-sliced)
+        # or "legacy" (mma.sync, whole K); 128-k stages per K slice of the tcgen05 kernel
+        self.w2_decode = os.environ.get("MOET_W2_DECODE", "legacy")
+        self.w2_tcd_spt = int(os.environ.get("MOET_W2_TCD_SPT", "8"))
 
     # ------------------------------------------------------------------ helpers
     @staticmethod
@@ -193,6 +197,10 @@ class NativeRunner:
         # vocab-parallel head: local (max, global id) per row, gathered, merged
         mv = self.ws.get("argmax.mv", (R, 2), torch.float32)
         self.C.argmax_split(logits, None, None, self.status, part, cnt, mv, self.tp_rank * logits.shape[1])
+        if self.ar is not None and 2 * R <= self.ar.cap:
+            # one kernel: push the pairs to every peer over NVLink, wait, merge in rank order
+            self.C.argmax_merge_ar(mv, ids, self.ar.desc)
+            return
         allmv = self.ws.get("argmax.all", (self.tp_size, R, 2), torch.float32)
         torch.distributed.all_gather_into_tensor(allmv, mv, group=self.tp_group)
         self.C.argmax_merge(allmv, ids)
@@ -205,13 +213,16 @@ class NativeRunner:
         return w
 
     def set_tp_group(self, group, fused: Optional[bool] = None):
-        """Join a tensor-parallel group.  Decode-sized reductions then run fused
-        over peer memory (producer epilogues push, the next RMSNorm reduces);
-        prefill-sized ones use NCCL all-reduce.  MOET_TP_FUSED=1 enables the
-        fused path (default off: at TP2 on the DS4 shape it measured 6.93 ms per
-        decode step against 6.52 ms for NCCL all-reduce)."""
+        """Join a tensor-parallel group.  Decode-sized reductions (at most
+        MOET_TP_FUSED_MAX_T rows, default 8) run fused over peer memory: the
+        producing kernel's epilogue (streaming GEMV, expert combine) pushes its
+        partial into every peer, the next norm -- the streaming GEMV's fused-norm
+        prologue or rmsnorm_quant -- waits and reduces; the vocab-parallel argmax
+        merges over the same buffers.  Larger reductions use NCCL all-reduce.
+        MOET_TP_FUSED=1 turns the fused path on (off by default until measured on NVLink)."""
         import os
         self.tp_group = group
+        self.fused_max_t = int(os.environ.get("MOET_TP_FUSED_MAX_T", "8"))
         if fused is None:
             fused = os.environ.get("MOET_TP_FUSED", "0") == "1"
         if fused and group is not None:
@@ -311,7 +322,12 @@ class NativeRunner:
         if self.tp_group is None:
             self._gemv(aq, as_, lin, out, x)
         elif self._fused:
-            self.C.gemv_fp8(aq, as_, lin.w, lin.s, out, None, self.ar.desc)
+            K = lin.w.shape[-1]
+            if (T <= 8 and self.gemv_stream and lin.w.dim() == 2 and K % 128 == 0 and K <= 5120
+                    and aq.stride(0) % 16 == 0):
+                self.C.gemv_stream_fp8(aq, as_, lin.w, lin.s, out, None, self.status, ar_push=self.ar.desc)
+            else:
+                self.C.gemv_fp8(aq, as_, lin.w, lin.s, out, None, self.ar.desc)
             self._pend = (x, out)
         else:
             part = self.ws.get("rp_part", (T, self.cfg.hidden), torch.bfloat16)
@@ -347,12 +363,18 @@ class NativeRunner:
         qb = self.ws.get("qb", (T, Hh * (nope + rope)), torch.bfloat16)
         # decode: the input norms are fused into the streaming GEMVs' prologues (no separate
         # RMSNorm launches); needs no pending TP reduction and no indexer (which reads hq / qa)
-        fuse = (ctx.mode == "decode" and T <= 8 and self.gemv_stream and self._pend is None
+        fuse = (ctx.mode == "decode" and T <= 8 and self.gemv_stream and (self._pend is None or self._fused)
                 and lw.idx_wq is None and isinstance(lw.qkv_a.w, torch.Tensor) and lw.qkv_a.w.dim() == 2
                 and H % 128 == 0 and ql % 128 == 0 and H <= 5120 and ql <= 5120)
         if fuse:
             padd, self._pend_add = self._pend_add, None
-            if padd is not None:     # residual add of a pending TP reduction folded into the prologue
+            pend, self._pend = self._pend, None
+            if pend is not None:     # fused TP all-reduce completed in the prologue: x = resid + sum of partials
+                resid, xout = pend
+                assert xout.data_ptr() == x.data_ptr() and resid.is_contiguous()
+                C.gemv_stream_fp8(None, None, lw.qkv_a.w, lw.qkv_a.s, qkva, None, self.status, resid, lw.attn_norm,
+                                  cfg.rms_eps, None, xout, None, self.ar.desc)
+            elif padd is not None:     # residual add of a pending TP reduction folded into the prologue
                 x0, part, xout = padd
                 C.gemv_stream_fp8(None, None, lw.qkv_a.w, lw.qkv_a.s, qkva, None, self.status, x0, lw.attn_norm,
                                   cfg.rms_eps, part, xout)
@@ -574,6 +596,24 @@ class NativeRunner:
             q = bool(getattr(self.delta, "split", False))
             d13 = dict(pool8=self.delta.pool, codes_off8=o13, scale_off8=os13, slot_table8=t8, quintal=q)
             d2 = dict(pool8=self.delta.pool, codes_off8=o2, scale_off8=os2, slot_table8=t8, quintal=q)
+        if not d13 and self.w2_decode != "legacy" and MB in (8, 16):
+            # base-only experts: K-sliced outputs [slices, rows, N]; the consumers add the slices in order
+            def gemv(a, sa, gather, off_c, off_s, N, K, name):
+                if self.w2_decode == "tcd" and K % 128 == 0:     # tcgen05 block-scaled MMA
+                    ks = -(-(K // 128) // self.w2_tcd_spt)
+                    o = self.ws.get(name, (ks, R, N), torch.float32)
+                    C.moe_w2_tcd(a, sa, gather, pairs, npairs, ex.pool, off_c, off_s, ex.slot_table, o, N, K, MB,
+                                 self.miss, self.status)
+                else:                                            # mma.sync, scales folded into the lookup
+                    ks = -(-(K // 64) // 8)
+                    o = self.ws.get(name, (ks, R, N), torch.float32)
+                    C.moe_w2_gemv_split(a, sa, gather, pairs, npairs, ex.pool, off_c, off_s, ex.slot_table, o, N, K,
+                                        MB, self.miss)
+                return o
+            c13 = gemv(h2q, h2s, stok, L.off_codes13, L.off_sc13, 2 * I, H, "c13s")
+            a2q, a2s = self._fp8("a2", R, I)
+            C.swiglu_quant(c13, cfg.swiglu_limit or 0.0, None, 1, a2q, a2s)
+            return gemv(a2q, a2s, None, L.off_codes2, L.off_sc2, H, I, "y2s")
         c13 = self.ws.get("c13", (R, 2 * I), torch.float32)
         C.moe_w2_gemv(h2q, h2s, stok, pairs, npairs, ex.pool, L.off_codes13, L.off_sc13, ex.slot_table, c13,
                       2 * I, H, MB, self.miss, **d13)
@@ -594,7 +634,8 @@ class NativeRunner:
 
     def _layer(self, lw, x, ctx, cache, li):
         H = self.cfg.hidden
-        self._fused = self.ar is not None and ctx.mode == "decode" and self.ar.fits(ctx.T, H)
+        self._fused = (self.ar is not None and ctx.mode == "decode" and ctx.T <= self.fused_max_t
+                       and self.ar.fits(ctx.T, H))
         self._decode = ctx.mode == "decode"
         x2 = self.ws.get("x_mid", (ctx.T, H), torch.bfloat16)
         timed = self.timers is not None and ctx.mode in ("prefill", "cached")
