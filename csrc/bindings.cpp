@@ -46,10 +46,6 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
                  torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
                  c10::optional<torch::Tensor> miss_count, c10::optional<torch::Tensor> pool8, int64_t codes_off8,
                  int64_t scale_off8, c10::optional<torch::Tensor> slot_table8, bool quintal);
-void moe_w2_gemv_split(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor> gather, torch::Tensor pairs,
-                       torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
-                       torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
-                       c10::optional<torch::Tensor> miss_count);
 void moe_w2_tcd(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor> gather, torch::Tensor pairs,
                 torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
                 torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
@@ -166,7 +162,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out"), py::arg("N"), py::arg("K"), py::arg("rows_per_pair"), py::arg("miss_count"),
         py::arg("pool8") = py::none(), py::arg("codes_off8") = 0, py::arg("scale_off8") = 0,
         py::arg("slot_table8") = py::none(), py::arg("quintal") = false);
-  m.def("moe_w2_gemv_split", &moe_w2_gemv_split);
   m.def("moe_w2_tcd", &moe_w2_tcd);
   m.def("moe_combine", &moe_combine, py::arg("y"), py::arg("pos_of"), py::arg("wts"), py::arg("resid"),
         py::arg("shared_out"), py::arg("out"), py::arg("out_f32"), py::arg("ar") = py::none());

@@ -202,6 +202,71 @@ __global__ void router_logits_kernel(const __nv_bfloat16* __restrict__ x, int T,
   }
 }
 
+// Prefill router logits on the tensor cores: out[T, E] (f32) = x[T, H] (bf16) . w[E, H]^T (bf16),
+// fp32 accumulation -- the same operands and precision as the decode router above.  A CTA
+// computes a 64-token x 64-expert tile; 64-k slices of both operands are staged with
+// cp.async (double-buffered, rows padded by 16 bytes so ldmatrix is conflict-free) and
+// consumed by bf16 m16n8k16 MMAs, one 16-token strip per warp.
+__global__ void __launch_bounds__(128) router_logits_mma_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
+                                                                const __nv_bfloat16* __restrict__ w, int E,
+                                                                float* __restrict__ out) {
+  constexpr int BT = 64, BE = 64, BK = 64, LD = BK + 8;
+  __shared__ __align__(16) __nv_bfloat16 sx[2][BT * LD];
+  __shared__ __align__(16) __nv_bfloat16 sw[2][BE * LD];
+  const int t0 = blockIdx.x * BT, e0 = blockIdx.y * BE;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  auto load = [&](int buf, int k0, bool act) {
+    for (int i = tid; i < BT * BK / 8; i += 128) {
+      const int r = i >> 3, c = (i & 7) * 8;
+      const uint32_t dw = (uint32_t)__cvta_generic_to_shared(&sw[buf][r * LD + c]);
+      const __nv_bfloat16* srcw = w + (size_t)(e0 + r) * H + k0 + c;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dw), "l"(srcw) : "memory");
+      if (act) {
+        const bool ok = t0 + r < T;
+        const uint32_t dx = (uint32_t)__cvta_generic_to_shared(&sx[buf][r * LD + c]);
+        const __nv_bfloat16* srcx = ok ? x + (size_t)(t0 + r) * H + k0 + c : x;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dx), "l"(srcx), "r"(ok ? 16 : 0) : "memory");
+      }
+    }
+  };
+  // router weights are immutable: their first slice may load before the previous kernel ends
+  load(0, 0, false);
+  pdl_entry();
+  load(0, 0, true);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  float acc[8][4];
+#pragma unroll
+  for (int n = 0; n < 8; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  const int nk = H / BK;
+  for (int kc = 0; kc < nk; kc++) {
+    if (kc + 1 < nk) load((kc + 1) & 1, (kc + 1) * BK, true);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncthreads();
+    const __nv_bfloat16* ax = sx[kc & 1];
+    const __nv_bfloat16* bw = sw[kc & 1];
+#pragma unroll
+    for (int kk = 0; kk < BK / 16; kk++) {
+      uint32_t a[4];
+      ldmatrix_x4(a, ax + (warp * 16 + (lane & 15)) * LD + kk * 16 + (lane >> 4) * 8);
+#pragma unroll
+      for (int n = 0; n < 8; n++) {
+        uint32_t b[2];
+        ldmatrix_x2(b, bw + (n * 8 + (lane & 7)) * LD + kk * 16 + ((lane >> 3) & 1) * 8);
+        mma_bf16_16816(acc[n], a, b[0], b[1]);
+      }
+    }
+    __syncthreads();
+  }
+  const int r0 = t0 + warp * 16 + g;
+#pragma unroll
+  for (int n = 0; n < 8; n++) {
+    const int col = e0 + n * 8 + 2 * t;
+    if (r0 < T) *reinterpret_cast<float2*>(out + (size_t)r0 * E + col) = make_float2(acc[n][0], acc[n][1]);
+    if (r0 + 8 < T) *reinterpret_cast<float2*>(out + (size_t)(r0 + 8) * E + col) = make_float2(acc[n][2], acc[n][3]);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Pair-list builder.  outputs:
 //   sorted_tok[R]   token of each expert-sorted row
@@ -461,6 +526,12 @@ void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out) {
               w.is_contiguous() && H % 256 == 0, "router_logits: bf16 contiguous, H % 256 == 0");
   if (T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
+  if (T > 64 && E % 64 == 0 && H % 64 == 0 && out.is_contiguous()) {   // prefill-sized: tensor-core tiles
+    launch_k(router_logits_mma_kernel, dim3((T + 63) / 64, E / 64), 128, 0, stream, (const __nv_bfloat16*)x.data_ptr(),
+             T, H, (const __nv_bfloat16*)w.data_ptr(), E, out.data_ptr<float>());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   launch_k(router_logits_kernel, (E + 7) / 8, 256, 0, stream, (const __nv_bfloat16*)x.data_ptr(), T, H,
                                                         (const __nv_bfloat16*)w.data_ptr(), E, out.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -264,206 +264,6 @@ __global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Arg
 }
 
 
-// ---------------------------------------------------------------------------------------
-// Decode GEMV over the 2-bit base (no delta tier), issue-lean variant.
-//
-// The legacy kernel above spends most of its issue slots on scale arithmetic: two
-// accumulator fragments per k64 chunk, four UE8M0 decodes and twelve FMAs.  Here the
-// weight block scale is folded into the lookup word itself.  Per (row, k32 group) the
-// word holds the four e4m3 levels {-4,-1,+1,+4} * 2^(e - base), base = the task's largest
-// scale exponent - 6 (so +4 * 2^6 = 256 stays inside e4m3); for e - base >= -6 the word
-// is L + (e - base) * 0x08080808 (a per-byte exponent add), below that the exact
-// subnormal / zero bytes.  Both k32 MMAs of a chunk then chain into one accumulator and
-// one FMA per output applies the activation's per-64 scale; the 2^base factor is applied
-// once at the end (exact: powers of two).
-//
-// Work is split into tasks (pair, 16-row block, K slice) handed to persistent warps in a
-// grid-stride loop over the device-side pair count, so the tail of a decode step (a
-// handful of routed experts) still fills every SM.  Slice s writes its partial sums to
-// out + s * part_stride; the consumers (swiglu_quant, moe_combine) add the slices in
-// slice order, so results do not depend on scheduling.
-struct W2SplitArgs {
-  const uint8_t* A; const uint8_t* sA; long long a_stride;
-  const int* gather;
-  const int4* pairs; const int* n_pairs;
-  const uint8_t* pool; long long slot_bytes, codes_off, scale_off;
-  const int* slot_table;
-  float* out; long long out_stride, part_stride;
-  int N, K, ksplit, cps;     // K slices, 64-k chunks per slice
-  int* miss_count;
-};
-
-constexpr int kW2sMaxCps = 8;     // chunks per slice: one batch of code loads per task
-
-MOET_DEVICE uint32_t e4m3_pow2(int m) {   // e4m3 byte of 2^m (exact down to 2^-9, 0 below)
-  return m >= -6 ? (uint32_t)((m + 7) << 3) : (m >= -9 ? (1u << (m + 9)) : 0u);
-}
-
-// Task order: pair (slowest), K slice, 16-row block (fastest).  Each warp takes one
-// contiguous range of tasks, so consecutive tasks mostly share (pair, slice): the
-// activation scales are staged once per change, and the next task's codes and block
-// scales are loaded into registers while the current task computes.
-template <int NT>
-__global__ void __launch_bounds__(128) moe_w2_gemv_split_kernel(W2SplitArgs p) {
-  pdl_entry();
-  extern __shared__ __align__(16) uint8_t w2s_smem[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int nwc = blockDim.x >> 5;
-  uint4* lut = reinterpret_cast<uint4*>(w2s_smem) + (size_t)warp * kW2sMaxCps * 8;          // [chunk][g]
-  float* asc = reinterpret_cast<float*>(w2s_smem + (size_t)nwc * kW2sMaxCps * 8 * 16) +
-               (size_t)warp * kW2sMaxCps * NT * 8;                                              // [chunk][token]
-  const int NB = p.N >> 4, KC = p.K >> 6, KS = p.K >> 5;
-  const long long total = (long long)(*p.n_pairs) * p.ksplit * NB;
-  const long long nw = (long long)gridDim.x * nwc;
-  const long long per = (total + nw - 1) / nw;
-  const long long tb = ((long long)blockIdx.x * nwc + warp) * per, te = min(total, tb + per);
-  constexpr uint32_t L = 0x4838B8C8u;   // e4m3 {-4, -1, +1, +4}
-
-  // task -> (pair, slice, block) and the pair's slot / rows (cached across tasks of one pair)
-  int cpi = -1, cslot = -1;
-  int4 cpr = make_int4(0, 0, 0, 0);
-  auto resolve = [&](long long task, int& pi, int& sl, int& nb) {
-    nb = (int)(task % NB);
-    const long long r = task / NB;
-    sl = (int)(r % p.ksplit);
-    pi = (int)(r / p.ksplit);
-    if (pi != cpi) { cpi = pi; cpr = p.pairs[pi]; cslot = p.slot_table[cpr.x]; }
-  };
-  auto load = [&](long long task, uint2 (&wv)[kW2sMaxCps], uint4& sv) {
-    int pi, sl, nb;
-    resolve(task, pi, sl, nb);
-    if (cslot < 0) return;
-    const int c0 = sl * p.cps, nc = min(KC, c0 + p.cps) - c0;
-    const uint8_t* base = p.pool + (size_t)cslot * p.slot_bytes;
-    const uint8_t* codes = base + p.codes_off + ((size_t)nb * KC + c0) * 256 + lane * 8;
-#pragma unroll
-    for (int u = 0; u < kW2sMaxCps; u++)
-      if (u < nc) wv[u] = ldg_stream_u2(codes + (size_t)u * 256);
-    if (lane < 2 * nc)
-      sv = __ldg(reinterpret_cast<const uint4*>(base + p.scale_off + (size_t)nb * KS * 16 + (size_t)c0 * 32) + lane);
-  };
-
-  uint2 wv[kW2sMaxCps], wn[kW2sMaxCps];
-  uint4 sv = make_uint4(0, 0, 0, 0), sn = make_uint4(0, 0, 0, 0);
-  if (tb < te) load(tb, wv, sv);
-  int key = -1;             // (pair, slice) whose activation scales are staged
-  int xr[NT];
-  for (long long task = tb; task < te; task++) {
-    int pi, sl, nb;
-    resolve(task, pi, sl, nb);
-    const int slot = cslot, r0 = cpr.y, nrows = cpr.z;
-    float* outs = p.out + (size_t)sl * p.part_stride;
-    const int c0 = sl * p.cps, nc = min(KC, c0 + p.cps) - c0;
-    if (slot < 0 || nc <= 0) {
-      if (slot < 0 && nb == 0 && sl == 0 && lane == 0 && p.miss_count) atomicAdd(p.miss_count, 1);
-      for (int j = 0; j < nrows; j++)
-        if (lane < 16) outs[(size_t)(r0 + j) * p.out_stride + nb * 16 + lane] = 0.f;
-      if (task + 1 < te) {
-        load(task + 1, wv, sv);
-        resolve(task, pi, sl, nb);      // restore the cached pair of this task
-      }
-      continue;
-    }
-    __syncwarp();           // the previous task's reads of the stages are done
-    if (pi * p.ksplit + sl != key) {
-      key = pi * p.ksplit + sl;
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++) {
-        const int j = nt * 8 + g;
-        xr[nt] = j < nrows ? (p.gather ? __ldg(p.gather + r0 + j) : r0 + j) : -1;
-      }
-      for (int i = lane; i < nc * NT * 8; i += 32) {
-        const int cl = i / (NT * 8), j = i % (NT * 8);
-        float v = 0.f;
-        if (j < nrows) {
-          const int ar = p.gather ? __ldg(p.gather + r0 + j) : r0 + j;
-          v = ue8m0_to_float(__ldg(p.sA + (size_t)ar * KC + c0 + cl));
-        }
-        asc[i] = v;
-      }
-    }
-    // fold the block scales into the lookup words
-    uint32_t mx = 0u, mn = 0xFFFFFFFFu;
-    if (lane < 2 * nc) {
-      mx = __vmaxu4(__vmaxu4(sv.x, sv.y), __vmaxu4(sv.z, sv.w));
-      mn = __vminu4(__vminu4(sv.x, sv.y), __vminu4(sv.z, sv.w));
-      mx = max(max(mx & 0xFFu, (mx >> 8) & 0xFFu), max((mx >> 16) & 0xFFu, mx >> 24));
-      mn = min(min(mn & 0xFFu, (mn >> 8) & 0xFFu), min((mn >> 16) & 0xFFu, mn >> 24));
-    }
-    mx = __reduce_max_sync(0xFFFFFFFFu, mx);
-    mn = __reduce_min_sync(0xFFFFFFFFu, mn);
-    const int eb = (int)mx - 6;                  // biased exponent of the folded base
-    const bool fast = (int)mn - eb >= -6;        // every level is a normal e4m3 number
-    if (lane < 2 * nc) {
-      uint32_t* lw = reinterpret_cast<uint32_t*>(lut) + ((lane >> 1) * 8 << 2) + (lane & 1) * 2;
-      const uint32_t wds[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-      for (int r = 0; r < 16; r++) {
-        const int d = (int)((wds[r >> 2] >> ((r & 3) * 8)) & 0xFFu) - eb;
-        uint32_t word;
-        if (fast) {
-          word = L + (uint32_t)d * 0x08080808u;
-        } else {
-          const uint32_t p1 = e4m3_pow2(d), p4 = e4m3_pow2(d + 2);
-          word = (p4 << 24) | (p1 << 16) | ((p1 | 0x80u) << 8) | (p4 | 0x80u);
-        }
-        lw[((r & 7) << 2) + (r >> 3)] = word;
-      }
-    }
-    __syncwarp();
-    // the next task's codes and scales stream in while this one computes
-    if (task + 1 < te) {
-      load(task + 1, wn, sn);
-      resolve(task, pi, sl, nb);
-    }
-    float acc[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-#pragma unroll
-    for (int u = 0; u < kW2sMaxCps; u++) {
-      if (u >= nc) break;
-      const uint4 L4 = lut[u * 8 + g];
-      const uint32_t mlo = wv[u].x & 0x33333333u, mhi = wv[u].y & 0x33333333u;
-      const uint32_t nlo = (wv[u].x >> 2) & 0x33333333u, nhi = (wv[u].y >> 2) & 0x33333333u;
-      const uint32_t A0[4] = {prmt(L4.x, L4.x, mlo), prmt(L4.y, L4.y, mhi), prmt(L4.x, L4.x, nlo),
-                              prmt(L4.y, L4.y, nhi)};
-      const uint32_t A1[4] = {prmt(L4.z, L4.z, mlo >> 16), prmt(L4.w, L4.w, mhi >> 16),
-                              prmt(L4.z, L4.z, nlo >> 16), prmt(L4.w, L4.w, nhi >> 16)};
-      const int c = c0 + u;
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++) {
-        uint2 xa = make_uint2(0, 0), xb = make_uint2(0, 0);
-        if (xr[nt] >= 0) {
-          const uint8_t* xp = p.A + (size_t)xr[nt] * p.a_stride + (size_t)c * 64 + 8 * t;
-          xa = __ldg(reinterpret_cast<const uint2*>(xp));
-          xb = __ldg(reinterpret_cast<const uint2*>(xp + 32));
-        }
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
-        mma_e4m3_16832(d, A0, xa.x, xa.y, d);
-        mma_e4m3_16832(d, A1, xb.x, xb.y, d);
-        const float2 s2 = *reinterpret_cast<const float2*>(asc + (u * NT + nt) * 8 + 2 * t);
-        acc[nt][0] = fmaf(d[0], s2.x, acc[nt][0]);
-        acc[nt][1] = fmaf(d[1], s2.y, acc[nt][1]);
-        acc[nt][2] = fmaf(d[2], s2.x, acc[nt][2]);
-        acc[nt][3] = fmaf(d[3], s2.y, acc[nt][3]);
-      }
-    }
-    const float bs = eb >= 1 ? __uint_as_float((uint32_t)eb << 23) : ldexpf(1.f, eb - 127);
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const int j = nt * 8 + 2 * t + (i & 1);
-        if (j >= nrows) continue;
-        const int row = nb * 16 + g + ((i & 2) ? 8 : 0);
-        outs[(size_t)(r0 + j) * p.out_stride + row] = acc[nt][i] * bs;
-      }
-#pragma unroll
-    for (int u = 0; u < kW2sMaxCps; u++) wv[u] = wn[u];
-    sv = sn;
-  }
-}
-
 // out[t, :] = resid[t] (+ shared[t]) + sum_j w[t, j] * y[pos_of[t*k + j], :]  (fixed j order)
 __global__ void moe_combine_kernel(const float* __restrict__ y, const int* __restrict__ pos_of,
                                    const float* __restrict__ wts, int k, int H,
@@ -591,49 +391,5 @@ void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::
                                             (const __nv_bfloat16*)opt_ptr(resid), (const __nv_bfloat16*)opt_ptr(shared_out),
                                             (__nv_bfloat16*)opt_ptr(out), (float*)opt_ptr(out_f32), ar_on, d,
                                             nsplit, split_stride);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
-
-// Decode expert GEMV over the 2-bit base, K-sliced: out [ksplit, rows, N] f32 partials.
-void moe_w2_gemv_split(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor> gather, torch::Tensor pairs,
-                       torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
-                       torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
-                       c10::optional<torch::Tensor> miss_count) {
-  TORCH_CHECK(K % 64 == 0 && N % 16 == 0, "moe_w2_gemv_split: N % 16, K % 64");
-  TORCH_CHECK(a.stride(1) == 1 && a.size(1) == K && a.stride(0) % 8 == 0, "moe_w2_gemv_split: A [rows, K]");
-  TORCH_CHECK(sa.is_contiguous() && sa.size(1) == K / 64, "moe_w2_gemv_split: sA [rows, K/64]");
-  TORCH_CHECK(out.dim() == 3 && out.scalar_type() == at::kFloat && out.stride(2) == 1 && out.size(2) == N,
-              "moe_w2_gemv_split: out [ksplit, rows, N] f32");
-  TORCH_CHECK(pool.dim() == 2 && codes_off % 16 == 0 && scale_off % 16 == 0 && pool.stride(0) % 16 == 0,
-              "moe_w2_gemv_split: pool alignment");
-  const int KC = K / 64, ks = out.size(0);
-  const int cps = (KC + ks - 1) / ks;
-  TORCH_CHECK(ks >= 1 && cps <= kW2sMaxCps, "moe_w2_gemv_split: at most 8 chunks (512 k) per slice");
-  W2SplitArgs p;
-  p.A = (const uint8_t*)a.data_ptr(); p.sA = (const uint8_t*)sa.data_ptr(); p.a_stride = a.stride(0);
-  p.gather = gather.has_value() && gather->defined() ? gather->data_ptr<int>() : nullptr;
-  p.pairs = (const int4*)pairs.data_ptr<int>(); p.n_pairs = n_pairs.data_ptr<int>();
-  p.pool = (const uint8_t*)pool.data_ptr(); p.slot_bytes = pool.stride(0);
-  p.codes_off = codes_off; p.scale_off = scale_off;
-  p.slot_table = slot_table.data_ptr<int>();
-  p.out = out.data_ptr<float>(); p.out_stride = out.stride(1); p.part_stride = out.stride(0);
-  p.N = N; p.K = K; p.ksplit = ks; p.cps = cps;
-  p.miss_count = miss_count.has_value() && miss_count->defined() ? miss_count->data_ptr<int>() : nullptr;
-  auto stream = at::cuda::getCurrentCUDAStream();
-  const int wpc = 4;
-  static int n_sm = 0;
-  if (!n_sm) cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, 0);
-  auto launch = [&](auto kern, int nt) {
-    const size_t smem = (size_t)wpc * (kW2sMaxCps * 8 * 16 + kW2sMaxCps * nt * 8 * 4);
-    int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpc * 32, smem);
-    launch_k(kern, std::max(1, per_sm) * n_sm, wpc * 32, smem, stream, p);
-  };
-  switch (rows_per_pair) {
-    case 8: launch(moe_w2_gemv_split_kernel<1>, 1); break;
-    case 16: launch(moe_w2_gemv_split_kernel<2>, 2); break;
-    case 32: launch(moe_w2_gemv_split_kernel<4>, 4); break;
-    default: TORCH_CHECK(false, "moe_w2_gemv_split: rows_per_pair must be 8/16/32");
-  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -193,7 +193,7 @@ def test_moe_w2_scale_folding_wide_exponent_range(C):
             assert rel(out[int(posof[t * 2 + j])].cpu(), A[t] @ W.t()) < 1e-4
 
 
-@pytest.mark.parametrize("impl", ["split", "tcd"])
+@pytest.mark.parametrize("impl", ["tcd"])
 @pytest.mark.parametrize("T,k,E,N,K,MB,ks,lo,hi", [(1, 8, 16, 64, 256, 8, 2, 122, 130),
                                                    (3, 8, 16, 128, 4096, 8, 8, 100, 130),
                                                    (40, 4, 8, 64, 192, 16, 3, 122, 130),
@@ -201,18 +201,14 @@ def test_moe_w2_scale_folding_wide_exponent_range(C):
                                                    (2, 8, 16, 32, 512, 8, 1, 60, 131),
                                                    (20, 4, 8, 208, 384, 16, 3, 118, 132),
                                                    (3, 8, 16, 64, 1536, 8, 5, 120, 132)])
-def test_moe_w2_gemv_split(C, impl, T, k, E, N, K, MB, ks, lo, hi):
-    """The K-sliced decode expert GEMVs -- mma.sync with the block scales folded into the
-    lookup words ("split"), and the tcgen05 block-scaled MMA ("tcd") -- summed over their
-    slices in order equal the fp64 dequantised reference, including scale ranges wide
-    enough to need subnormal / flushed levels in the folded form, partial 128-row tiles
-    and slices past the end of K; a missing expert gives zero rows and a miss count.  The
-    split-aware consumers (swiglu_quant, moe_combine) equal their one-slice results on the
-    summed tensor."""
+def test_moe_w2_tcd_sliced(C, impl, T, k, E, N, K, MB, ks, lo, hi):
+    """The K-sliced tcgen05 decode expert GEMV (block-scaled MMA, scales in TMEM) summed over
+    its slices in order equals the fp64 dequantised reference, over wide scale ranges,
+    partial 128-row tiles and slices past the end of K; a missing expert gives zero rows
+    and a miss count.  The split-aware consumers (swiglu_quant, moe_combine) equal their
+    one-slice results on the summed tensor."""
     if impl == "tcd" and (K % 128 or MB not in (8, 16)):
         pytest.skip("tcgen05 decode kernel: K % 128 == 0, 8 or 16 rows per pair")
-    if impl == "split" and -(-(K // 64) // ks) > 8:
-        pytest.skip("mma.sync split kernel: at most 8 chunks per slice")
     g = torch.Generator().manual_seed(T * 131 + K)
     codes, sc, pool = _expert_pool(E, N, K, g, lo=lo, hi=hi)
     ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).int()
@@ -230,12 +226,8 @@ def test_moe_w2_gemv_split(C, impl, T, k, E, N, K, MB, ks, lo, hi):
     slot_table = torch.arange(E, dtype=torch.int32, device=DEV)
     miss = torch.zeros(1, dtype=torch.int32, device=DEV)
     def run():
-        if impl == "tcd":
-            C.moe_w2_tcd(qw2, dev(s), stok, pairs, npairs, dev(pool), 0, N * K // 4, slot_table, out, N, K, MB, miss,
-                         status)
-        else:
-            C.moe_w2_gemv_split(qw2, dev(s), stok, pairs, npairs, dev(pool), 0, N * K // 4, slot_table, out, N, K,
-                                MB, miss)
+        C.moe_w2_tcd(qw2, dev(s), stok, pairs, npairs, dev(pool), 0, N * K // 4, slot_table, out, N, K, MB, miss,
+                     status)
     run()
     tot = out.sum(0).cpu().double()
     A = fp8.dequant_act_fp8(q, s).double()
@@ -246,8 +238,7 @@ def test_moe_w2_gemv_split(C, impl, T, k, E, N, K, MB, ks, lo, hi):
             W = codebook.dequant_codes(codes[e], sc[e]).double()
             ref = A[t] @ W.t()
             # levels 2^-10 below a group's block maximum flush: bounded by the largest term
-            tol = 1e-4 if (hi - lo < 16 or impl == "tcd") else 2e-3
-            assert rel(tot[posof_c[t * k + j]], ref) < tol, (t, j)
+            assert rel(tot[posof_c[t * k + j]], ref) < 1e-4, (t, j)
     assert int(miss) == 0 and int(status) == 0
     # split-aware consumers
     if N % 128 == 0:
@@ -452,10 +443,12 @@ def test_rmsnorm_quant_output_stride(C):
     assert torch.equal(q[:, H:], qa) and torch.equal(s[:, H // 64:], sa)
 
 
-@pytest.mark.parametrize("T", [1, 3, 20])
-def test_router_logits(C, T):
+@pytest.mark.parametrize("T,E", [(1, 256), (3, 256), (20, 256), (65, 256), (1000, 384), (130, 64)])
+def test_router_logits(C, T, E):
+    """Decode-sized (warp per expert) and prefill-sized (tensor-core tiles, T > 64) router
+    logits against the fp32 product of the same bf16 operands."""
     g = torch.Generator().manual_seed(T)
-    E, H = 256, 4096
+    H = 4096
     x = torch.randn(T, H, generator=g).to(torch.bfloat16)
     w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16)
     out = torch.empty(T, E, device=DEV)

@@ -138,8 +138,9 @@ class NativeRunner:
         self.mb8_max_r = int(os.environ.get("MOET_MB8_MAX_R", "2048"))
         # decode experts on the tcgen05 kernel with this token tile (0: mma.sync GEMV)
         self.decode_tc_nt = int(os.environ.get("MOET_DECODE_TC_NT", "0"))
-        # decode experts over the 2-bit base: "tcd" (tcgen05, K-sliced), "split" (mma.sync, K-sliced)
-        # or "legacy" (mma.sync, whole K); 128-k stages per K slice of the tcgen05 kernel
+        # decode experts over the 2-bit base: "legacy" (mma.sync GEMV, default) or "tcd" (tcgen05
+        # block-scaled, K-sliced; measured slower at 1-32 streams, see moe_w2_tcd.cu); 128-k stages
+        # per K slice of the tcgen05 kernel
         self.w2_decode = os.environ.get("MOET_W2_DECODE", "legacy")
         self.w2_tcd_spt = int(os.environ.get("MOET_W2_TCD_SPT", "8"))
 
@@ -504,10 +505,8 @@ class NativeRunner:
             self._ensure_experts(mli, ids)
             y2 = self._moe_gemv_pairs(h2q, h2s, stok, pairs, npairs, ex, R, MB, mli)
         else:
-            if T <= 64:
-                C.router_logits(hb, self._router_w(lw), logits)
-            else:   # prefill: a plain GEMM, cuBLAS in fp32
-                torch.mm(hb.float(), lw.router_w.t(), out=logits)
+            # bf16 operands, fp32 accumulation; prefill-sized T runs on tensor-core tiles
+            C.router_logits(hb, self._router_w(lw), logits)
             C.router_topk(logits, lw.router_bias, k, cfg.router == "sigmoid", cfg.n_group, cfg.topk_group,
                           cfg.norm_topk_prob, cfg.routed_scaling, ids, wts)
             if topp > 0:        # expert top-p pruning: the tail moves to the top-1 expert with weight 0
@@ -596,19 +595,18 @@ class NativeRunner:
             q = bool(getattr(self.delta, "split", False))
             d13 = dict(pool8=self.delta.pool, codes_off8=o13, scale_off8=os13, slot_table8=t8, quintal=q)
             d2 = dict(pool8=self.delta.pool, codes_off8=o2, scale_off8=os2, slot_table8=t8, quintal=q)
-        if not d13 and self.w2_decode != "legacy" and MB in (8, 16):
+        if not d13 and self.w2_decode == "tcd" and MB in (8, 16):
             # base-only experts: K-sliced outputs [slices, rows, N]; the consumers add the slices in order
             def gemv(a, sa, gather, off_c, off_s, N, K, name):
-                if self.w2_decode == "tcd" and K % 128 == 0:     # tcgen05 block-scaled MMA
-                    ks = -(-(K // 128) // self.w2_tcd_spt)
-                    o = self.ws.get(name, (ks, R, N), torch.float32)
-                    C.moe_w2_tcd(a, sa, gather, pairs, npairs, ex.pool, off_c, off_s, ex.slot_table, o, N, K, MB,
-                                 self.miss, self.status)
-                else:                                            # mma.sync, scales folded into the lookup
-                    ks = -(-(K // 64) // 8)
-                    o = self.ws.get(name, (ks, R, N), torch.float32)
-                    C.moe_w2_gemv_split(a, sa, gather, pairs, npairs, ex.pool, off_c, off_s, ex.slot_table, o, N, K,
-                                        MB, self.miss)
+                if K % 128:                                      # the tcgen05 kernel streams 128-k stages
+                    o = self.ws.get(name + ".l", (R, N), torch.float32)
+                    C.moe_w2_gemv(a, sa, gather, pairs, npairs, ex.pool, off_c, off_s, ex.slot_table, o, N, K, MB,
+                                  self.miss)
+                    return o
+                ks = -(-(K // 128) // self.w2_tcd_spt)
+                o = self.ws.get(name, (ks, R, N), torch.float32)
+                C.moe_w2_tcd(a, sa, gather, pairs, npairs, ex.pool, off_c, off_s, ex.slot_table, o, N, K, MB,
+                             self.miss, self.status)
                 return o
             c13 = gemv(h2q, h2s, stok, L.off_codes13, L.off_sc13, 2 * I, H, "c13s")
             a2q, a2s = self._fp8("a2", R, I)
