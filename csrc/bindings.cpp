@@ -45,14 +45,21 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
                  torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
                  torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
                  c10::optional<torch::Tensor> miss_count, c10::optional<torch::Tensor> pool8, int64_t codes_off8,
-                 int64_t scale_off8, c10::optional<torch::Tensor> slot_table8, bool quintal);
+                 int64_t scale_off8, c10::optional<torch::Tensor> slot_table8, bool quintal,
+                 c10::optional<torch::Tensor> ep, c10::optional<torch::Tensor> ret_rows);
+void ep_dispatch(torch::Tensor desc, torch::Tensor xq, torch::Tensor xs, torch::Tensor ids);
+void ep_recv_pairs(torch::Tensor desc, int64_t MB, torch::Tensor ids, torch::Tensor rank_scratch,
+                   torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
+                   torch::Tensor n_rows);
+int64_t ep_buffer_bytes(int64_t world, int64_t cap, int64_t H);
 void moe_w2_tcd(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor> gather, torch::Tensor pairs,
                 torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
                 torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
                 c10::optional<torch::Tensor> miss_count, torch::Tensor status);
 void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::optional<torch::Tensor> resid,
                  c10::optional<torch::Tensor> shared_out, c10::optional<torch::Tensor> out,
-                 c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> ar);
+                 c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> ar,
+                 c10::optional<torch::Tensor> ep);
 // gemv_stream.cu
 void gemv_stream_fp8(c10::optional<torch::Tensor> a, c10::optional<torch::Tensor> sa, torch::Tensor w,
                      torch::Tensor sw, torch::Tensor out, c10::optional<torch::Tensor> resid, torch::Tensor status,
@@ -161,10 +168,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("n_pairs"), py::arg("pool"), py::arg("codes_off"), py::arg("scale_off"), py::arg("slot_table"),
         py::arg("out"), py::arg("N"), py::arg("K"), py::arg("rows_per_pair"), py::arg("miss_count"),
         py::arg("pool8") = py::none(), py::arg("codes_off8") = 0, py::arg("scale_off8") = 0,
-        py::arg("slot_table8") = py::none(), py::arg("quintal") = false);
+        py::arg("slot_table8") = py::none(), py::arg("quintal") = false, py::arg("ep") = py::none(),
+        py::arg("ret_rows") = py::none());
   m.def("moe_w2_tcd", &moe_w2_tcd);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_recv_pairs", &ep_recv_pairs);
+  m.def("ep_buffer_bytes", &ep_buffer_bytes);
   m.def("moe_combine", &moe_combine, py::arg("y"), py::arg("pos_of"), py::arg("wts"), py::arg("resid"),
-        py::arg("shared_out"), py::arg("out"), py::arg("out_f32"), py::arg("ar") = py::none());
+        py::arg("shared_out"), py::arg("out"), py::arg("out_f32"), py::arg("ar") = py::none(),
+        py::arg("ep") = py::none());
   m.def("bf12_decode", &bf12_decode);
   m.def("indexer_logits", &indexer_logits);
   m.def("indexer_topk", &indexer_topk);

@@ -12,6 +12,7 @@
 // captured CUDA graph replays any routing.  Numerics do not depend on the
 // order of rows inside an expert (each output column is independent).
 #include "common.cuh"
+#include "ep_a2a.cuh"
 #include "torch_glue.h"
 
 namespace moet {
@@ -354,6 +355,30 @@ __global__ void build_pairs_kernel(const int* __restrict__ topk_ids, int R, int 
                     e_lo, ep);
 }
 
+// Expert parallelism, owner side (protocol in ep_a2a.cuh).  One CTA of 1024 threads:
+// bounded wait for every source's dispatch flag, then the expert pair list of the rows
+// received -- ids[r] = local expert id of received row r = src * cap + i, -1 for empty
+// slots (skipped) -- with sorted row -> received row index in sorted_tok.
+__global__ void __launch_bounds__(1024) ep_recv_pairs_kernel(EpDesc d, int MB, int* __restrict__ ids,
+                                                             int* __restrict__ rank_scratch,
+                                                             int* __restrict__ sorted_tok, int* __restrict__ pos_of,
+                                                             int4* __restrict__ pairs, int* __restrict__ n_pairs,
+                                                             int* __restrict__ n_rows) {
+  pdl_entry();
+  const unsigned long long epoch = ep_epoch(d);
+  const bool ok = ep_wait(d, epoch, 0);
+  const int R = d.world * d.cap;
+  const int* nrows = ep_nrows(d, d.rank);
+  const int* meta = ep_meta(d, d.rank);
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    const int src = r / d.cap, i = r - src * d.cap;
+    ids[r] = ok && i < nrows[src] ? meta[r] : -1;
+  }
+  __syncthreads();
+  build_pairs_block(ids, R, 1, d.E_loc, MB, rank_scratch, sorted_tok, pos_of, pairs, n_pairs, d.status, 0, n_rows,
+                    0, 1);
+}
+
 // Decode routing in one launch: every CTA computes the router logits of 4
 // experts for all T tokens (4 warps per expert, each over a quarter of H;
 // bf16 x and W, fp32 sums; the weight rows are loaded before the dependency
@@ -568,6 +593,21 @@ void build_pairs(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor ra
                                              pos_of.data_ptr<int>(), (int4*)pairs.data_ptr<int>(),
                                              n_pairs.data_ptr<int>(), status.data_ptr<int>(), 0, (int*)nullptr,
                                              (int)std::max<int64_t>(e_lo, 0), e_lo >= 0 ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ep_recv_pairs(torch::Tensor desc, int64_t MB, torch::Tensor ids, torch::Tensor rank_scratch,
+                   torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
+                   torch::Tensor n_rows) {
+  EpDesc d = ep_desc_from(desc);
+  const int64_t R = (int64_t)d.world * d.cap;
+  TORCH_CHECK(d.E_loc <= kMaxE, "ep_recv_pairs: at most 512 local experts");
+  TORCH_CHECK(ids.numel() >= R && rank_scratch.numel() >= R && sorted_tok.numel() >= R && pos_of.numel() >= R &&
+              pairs.size(0) >= R / MB + std::min<int64_t>(d.E_loc, R), "ep_recv_pairs: buffers too small");
+  auto stream = at::cuda::getCurrentCUDAStream();
+  launch_k(ep_recv_pairs_kernel, 1, 1024, 0, stream, d, (int)MB, ids.data_ptr<int>(), rank_scratch.data_ptr<int>(),
+           sorted_tok.data_ptr<int>(), pos_of.data_ptr<int>(), (int4*)pairs.data_ptr<int>(), n_pairs.data_ptr<int>(),
+           n_rows.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -28,6 +28,7 @@
 //   per-warp 625-entry table, class offset from the code bits, one prmt over the
 //   e2m1 -> e4m3 magnitude pool, the sign bit from the base level.
 #include "common.cuh"
+#include "ep_a2a.cuh"
 #include "symm.cuh"
 #include "torch_glue.h"
 
@@ -47,6 +48,9 @@ struct W2Args {
   const uint8_t* pool8; long long slot_bytes8, codes_off8, scale_off8;
   const int* slot_table8;
   int quintal;                  // delta slots hold split-FP4 refinement planes (base codes + scales stay in use)
+  // expert parallelism, return leg: output row r (sorted) goes to the source rank's return
+  // row ret_rows[r] = src * cap + i (peer store), and the grid publishes a return flag
+  int ep_on; const int* ret_rows; EpDesc ep;
 };
 
 // 10-bit quintal word -> (d0 | d2 << 4) | (d1 | d3 << 4) << 8; x / 5 = (x * 0x334) >> 12 for x < 1024
@@ -68,8 +72,16 @@ MOET_DEVICE uint32_t quintal_reg(uint32_t csel, uint32_t Ta, uint32_t Tb, uint32
   return prmt(MLO, MHI, dsel + 5u * big) | (base & 0x80808080u);
 }
 
+// Destination of output row r0 + j: the local out matrix, or under expert parallelism the
+// source rank's return row in peer memory.
+MOET_DEVICE float* w2_out_row(const W2Args& p, int r) {
+  if (!p.ep_on) return p.out + (size_t)r * p.out_stride;
+  const int rr = p.ret_rows[r], src = rr / p.ep.cap;
+  return ep_ret(p.ep, src) + (size_t)(rr - src * p.ep.cap) * p.ep.H;
+}
+
 template <int NT>
-__global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Args p) {
+__device__ __forceinline__ void moe_w2_gemv_body(const W2Args& p) {
   pdl_entry();
   const int pi = blockIdx.y;
   if (pi >= *p.n_pairs) return;
@@ -84,7 +96,7 @@ __global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Arg
   if (slot < 0) {
     if (blockIdx.x == 0 && threadIdx.x == 0 && p.miss_count) atomicAdd(p.miss_count, 1);
     for (int j = 0; j < nrows; j++)
-      if (lane < 16) p.out[(size_t)(r0 + j) * p.out_stride + nb * 16 + lane] = 0.f;
+      if (lane < 16) w2_out_row(p, r0 + j)[nb * 16 + lane] = 0.f;
     return;
   }
   const int KC = p.K >> 6, KS = p.K >> 5;
@@ -259,8 +271,14 @@ __global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Arg
       const int j = nt * 8 + 2 * t + (i & 1);
       if (j >= nrows) continue;
       const int row = nb * 16 + g + ((i & 2) ? 8 : 0);
-      p.out[(size_t)(r0 + j) * p.out_stride + row] = acc[nt][i];
+      w2_out_row(p, r0 + j)[row] = acc[nt][i];
     }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(128, NT == 1 ? 8 : 4) moe_w2_gemv_kernel(W2Args p) {
+  moe_w2_gemv_body<NT>(p);
+  if (p.ep_on) ep_publish(p.ep, ep_epoch(p.ep), 1);   // every CTA, including ones with no work
 }
 
 
@@ -270,14 +288,17 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int* __res
                                    const __nv_bfloat16* __restrict__ resid,
                                    const __nv_bfloat16* __restrict__ shared_out,
                                    __nv_bfloat16* __restrict__ out, float* __restrict__ out_f32,
-                                   int ar_on, ArDesc ar, int nsplit, long long split_stride) {
+                                   int ar_on, ArDesc ar, int nsplit, long long split_stride,
+                                   int ep_on, EpDesc ep) {
   pdl_entry();
   const int tok = blockIdx.x;
   const unsigned long long epoch = ar_on ? ar_epoch(ar) : 0ull;
+  bool ep_ok = true;
+  if (ep_on) ep_ok = ep_wait(ep, ep_epoch(ep), 1);     // every owner has returned this rank's rows
   __shared__ int pos[32];
   __shared__ float w[32];
   if (threadIdx.x < k) {
-    pos[threadIdx.x] = pos_of[tok * k + threadIdx.x];
+    pos[threadIdx.x] = !ep_ok ? -1 : pos_of ? pos_of[tok * k + threadIdx.x] : tok * k + threadIdx.x;
     w[threadIdx.x] = wts[tok * k + threadIdx.x];
   }
   __syncthreads();
@@ -316,6 +337,17 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int* __res
     }
   }
   if (ar_on) ar_producer_arrive(ar, epoch);
+  if (ep_on) {   // the return rows are consumed: the last CTA closes the layer's epoch
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(ep.done, 1u) == gridDim.x * gridDim.y - 1) {
+        *ep.done = 0u;
+        *ep.ncall = *ep.ncall + 1ull;
+        __threadfence();
+      }
+    }
+  }
 }
 
 }  // namespace moet
@@ -326,7 +358,8 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
                  torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
                  torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
                  c10::optional<torch::Tensor> miss_count, c10::optional<torch::Tensor> pool8, int64_t codes_off8,
-                 int64_t scale_off8, c10::optional<torch::Tensor> slot_table8, bool quintal) {
+                 int64_t scale_off8, c10::optional<torch::Tensor> slot_table8, bool quintal,
+                 c10::optional<torch::Tensor> ep, c10::optional<torch::Tensor> ret_rows) {
   TORCH_CHECK(K % 64 == 0 && N % 16 == 0, "moe_w2_gemv: N % 16, K % 64");
   TORCH_CHECK(a.stride(1) == 1 && a.size(1) == K, "moe_w2_gemv: A [rows, K] inner-contiguous");
   TORCH_CHECK(sa.is_contiguous() && sa.size(1) == K / 64, "moe_w2_gemv: sA [rows, K/64]");
@@ -353,6 +386,14 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
     p.quintal = quintal ? 1 : 0;
     TORCH_CHECK(!quintal || codes_off8 % 8 == 0, "moe_w2_gemv: quintal plane offset");
   }
+  p.ep_on = ep.has_value() && ep->defined();
+  p.ret_rows = nullptr; p.ep = EpDesc{};
+  if (p.ep_on) {
+    p.ep = ep_desc_from(*ep);
+    TORCH_CHECK(ret_rows.has_value() && ret_rows->defined() && N == p.ep.H,
+                "moe_w2_gemv: the EP return leg needs ret_rows and N == H");
+    p.ret_rows = ret_rows->data_ptr<int>();
+  }
   const int max_pairs = pairs.size(0);
   const int wpc = 4;
   dim3 grid((N / 16 + wpc - 1) / wpc, max_pairs);
@@ -371,8 +412,13 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
 
 void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::optional<torch::Tensor> resid,
                  c10::optional<torch::Tensor> shared_out, c10::optional<torch::Tensor> out,
-                 c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> ar) {
-  // y: [R, H] or [nsplit, R, H] (K-slice partials, summed in slice order)
+                 c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> ar,
+                 c10::optional<torch::Tensor> ep) {
+  // y: [R, H] or [nsplit, R, H] (K-slice partials, summed in slice order); pos_of may be
+  // empty (identity: row t * k + j); ep: wait for the owners' returns first
+  const int ep_on = ep.has_value() && ep->defined();
+  EpDesc ed{};
+  if (ep_on) ed = ep_desc_from(*ep);
   const int T = wts.size(0), k = wts.size(1), H = y.size(-1);
   const int nsplit = y.dim() == 3 ? y.size(0) : 1;
   const long long split_stride = y.dim() == 3 ? y.stride(0) : 0;
@@ -387,9 +433,10 @@ void moe_combine(torch::Tensor y, torch::Tensor pos_of, torch::Tensor wts, c10::
   TORCH_CHECK(H % 4 == 0 && k <= 32, "moe_combine: H % 4, k <= 32");
   if (T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  launch_k(moe_combine_kernel, dim3(T, (H + 1023) / 1024), 256, 0, stream, y.data_ptr<float>(), pos_of.data_ptr<int>(), wts.data_ptr<float>(), k, H,
+  launch_k(moe_combine_kernel, dim3(T, (H + 1023) / 1024), 256, 0, stream, y.data_ptr<float>(),
+           pos_of.numel() ? pos_of.data_ptr<int>() : nullptr, wts.data_ptr<float>(), k, H,
                                             (const __nv_bfloat16*)opt_ptr(resid), (const __nv_bfloat16*)opt_ptr(shared_out),
                                             (__nv_bfloat16*)opt_ptr(out), (float*)opt_ptr(out_f32), ar_on, d,
-                                            nsplit, split_stride);
+                                            nsplit, split_stride, ep_on, ed);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

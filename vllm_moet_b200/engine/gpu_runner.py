@@ -114,6 +114,8 @@ class NativeRunner:
         self.tp_group = None
         self.tp_rank, self.tp_size = mw.tp_rank, mw.tp_size
         self.ar = None            # fused peer-memory all-reduce (SymmAllReduce) for decode-sized steps
+        self.ep = None            # expert-parallel all-to-all buffers (EpSymm) under DP attention + EP
+        self.ep_group = None
         self.cache = None         # residency.ExpertCache when routed experts are served from a host store
         self.delta = None         # residency.DeltaTier (FP4 hot experts) when enabled
         self._moe_index = {}
@@ -229,6 +231,83 @@ class NativeRunner:
         if fused and group is not None:
             from ..parallel.symm import SymmAllReduce
             self.ar = SymmAllReduce(group, 128 * self.cfg.hidden, self.dev, self.status)
+
+    def set_ep_group(self, group, cap_rows: int):
+        """Data-parallel attention + expert-parallel MoE: this rank holds the routed experts
+        [rank * E / W, (rank + 1) * E / W) and its own tokens.  Decode-sized MoE layers move
+        their rows over peer memory (dispatch kernel, owner's pair list, w2 GEMV epilogue
+        storing into the source's return rows, combine after a bounded wait); prefill-sized
+        ones use NCCL all-to-all.  ``cap_rows``: the most routed rows (tokens x top-k) of one
+        rank in one decode-sized layer."""
+        from ..parallel.symm import EpSymm
+        from ..residency import moe_layers
+        ex = moe_layers(self.mw)[0].experts
+        if ex.n_local is None:
+            raise ValueError("set_ep_group: the experts are not partitioned (parallel.ep.ep_partition)")
+        if self.cache is not None or self.delta is not None:
+            raise NotImplementedError("expert parallelism with the expert cache / delta tier")
+        self.ep_group = group
+        self.ep = EpSymm(group, cap_rows, self.cfg.hidden, ex.n_local, self.cfg.top_k, self.dev, self.status)
+
+    def _moe_ep_decode(self, h2q, h2s, ids, ex, MB):
+        """Decode-sized EP layer up to the owners' return stores (the caller's combine waits)."""
+        C, cfg, ep = self.C, self.cfg, self.ep
+        H, I = cfg.hidden, ex.layout.I
+        L = ex.layout
+        R = ep.world * ep.cap
+        P = R // MB + min(ep.E_loc, R)
+        idr = self.ws.get("ep.ids", (R,), torch.int32)
+        rank = self.ws.get("ep.rank", (R,), torch.int32)
+        stok = self.ws.get("ep.stok", (R,), torch.int32)
+        posof = self.ws.get("ep.posof", (R,), torch.int32)
+        pairs = self.ws.get("ep.pairs", (P, 4), torch.int32)
+        npairs = self.ws.get("ep.npairs", (1,), torch.int32)
+        nrows = self.ws.get("ep.nrows", (1,), torch.int32)
+        C.ep_dispatch(ep.desc, h2q, h2s, ids)
+        C.ep_recv_pairs(ep.desc, MB, idr, rank, stok, posof, pairs, npairs, nrows)
+        c13 = self.ws.get("ep.c13", (R, 2 * I), torch.float32)
+        C.moe_w2_gemv(ep.rx, ep.rs, stok, pairs, npairs, ex.pool, L.off_codes13, L.off_sc13, ex.slot_table, c13,
+                      2 * I, H, MB, self.miss)
+        a2q, a2s = self._fp8("ep.a2", R, I)
+        C.swiglu_quant(c13, cfg.swiglu_limit or 0.0, nrows, 1, a2q, a2s)
+        C.moe_w2_gemv(a2q, a2s, None, pairs, npairs, ex.pool, L.off_codes2, L.off_sc2, ex.slot_table, ep.ret,
+                      H, I, MB, self.miss, ep=ep.desc, ret_rows=stok)
+
+    def _moe_ep_prefill(self, h2q, h2s, ids, ex, T, MB):
+        """Prefill-sized EP layer with NCCL all-to-all (the parallel/ep.py algorithm) around
+        this rank's expert kernels -> [T * k, H] f32 expert outputs in (token, slot) order."""
+        import torch.distributed as dist
+        C, cfg, ep = self.C, self.cfg, self.ep
+        H, k, W = cfg.hidden, cfg.top_k, ep.world
+        flat = ids.reshape(-1).long()
+        dest = flat // ep.E_loc
+        order = torch.argsort(dest, stable=True)
+        send = torch.bincount(dest, minlength=W).to(torch.int64)
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.ep_group)
+        sc, rc = send.tolist(), recv.tolist()
+
+        def a2a(x, scnt, rcnt):
+            out = x.new_empty((sum(rcnt),) + tuple(x.shape[1:]))
+            dist.all_to_all_single(out, x.contiguous(), rcnt, scnt, group=self.ep_group)
+            return out
+        tok = torch.arange(T, device=ids.device).repeat_interleave(k)[order]
+        q = a2a(h2q[tok], sc, rc)
+        sq = a2a(h2s[tok], sc, rc)
+        lid = a2a((flat[order] - dest[order] * ep.E_loc).to(torch.int32), sc, rc)
+        Rr = q.shape[0]
+        yr = torch.zeros(Rr, H, dtype=torch.float32, device=ids.device)
+        if Rr:
+            L = ex.layout
+            tc = Rr >= self.tc_min_t and H % 128 == 0 and L.I % 128 == 0
+            y2, pos = (self._moe_tc(q, sq, lid.view(-1, 1), ex, Rr, Rr, ep.E_loc, -1) if tc else
+                       self._moe_gemv(q, sq, lid.view(-1, 1), ex, Rr, MB, None, ep.E_loc, -1))
+            one = torch.ones(Rr, 1, dtype=torch.float32, device=ids.device)
+            C.moe_combine(y2, pos, one, None, None, None, yr)
+        back = a2a(yr, rc, sc)
+        res = torch.empty(T * k, H, dtype=torch.float32, device=ids.device)
+        res[order] = back
+        return res
 
     def attach_expert_cache(self, cache):
         """Serve routed experts through `cache` (pools already rewired by
@@ -489,6 +568,24 @@ class NativeRunner:
         e_lo = ex.e_lo if ep else -1
         use_tc = ctx.mode in ("prefill", "cached") and H % 128 == 0 and I % 128 == 0 and (2 * I) % 128 == 0
         topp = self.ecfg.moet.topp
+        if self.ep is not None:
+            # DP attention + EP: route over all experts, then the all-to-all around the owners' kernels
+            C.router_logits(hb, self._router_w(lw), logits)
+            C.router_topk(logits, lw.router_bias, k, cfg.router == "sigmoid", cfg.n_group, cfg.topk_group,
+                          cfg.norm_topk_prob, cfg.routed_scaling, ids, wts)
+            fused = ctx.mode == "decode" and R <= self.ep.cap and ctx.mb in (8, 16, 32)
+            if fused:
+                self._moe_ep_decode(h2q, h2s, ids, ex, ctx.mb)
+            else:
+                yk = self._moe_ep_prefill(h2q, h2s, ids, ex, T, ctx.mb)
+            if sh is not None:
+                self._join()
+            none = self.ws.get("ep.nopos", (0,), torch.int32)
+            if fused:
+                C.moe_combine(self.ep.ret[:R], none, wts, x, sh, out, None, None, self.ep.desc)
+            else:
+                C.moe_combine(yk, none, wts, x, sh, out, None)
+            return
         if T <= 64 and not use_tc and H % 1024 == 0 and topp <= 0:
             # decode: logits + top-k + pair list in one launch
             MB = ctx.mb

@@ -76,9 +76,8 @@ class LLM:
             device = "cuda" if torch.cuda.is_available() else "cpu"
         self.device = torch.device(device)
         self._tp_group, self._pp_group = tp_group, pp_group
-        if self.device.type == "cuda" and (sp_group is not None or dcp_group is not None or ep_group is not None):
-            raise NotImplementedError("SP prefill / DCP decode / DP+EP run on the CPU engine; the GPU runner has "
-                                      "none of them yet")
+        if self.device.type == "cuda" and (sp_group is not None or dcp_group is not None):
+            raise NotImplementedError("SP prefill / DCP decode run on the CPU engine")
         self._ep_group = ep_group
         if speculative_method not in ("mtp", "dspark", "dflash", "eagle3"):
             raise ValueError(f"speculative_method {speculative_method!r}: mtp | dspark | dflash | eagle3")
@@ -164,7 +163,18 @@ class LLM:
             from .gpu_runner import DecodeState, NativeRunner
             nb = num_gpu_blocks or (max_num_seqs * self.max_blocks + 1)
             self.blocks = BlockManager(nb, prefix_caching=enable_prefix_caching)
+            if ep_group is not None:
+                import torch.distributed as dist
+                from ..parallel.ep import ep_partition
+                if expert_cache_slots or delta_slots or enable_prefix_caching or enable_chunked_prefill:
+                    raise NotImplementedError("GPU DP + EP: no expert cache, delta tier, prefix caching or "
+                                              "chunked prefill")
+                ep_partition(self.mw, dist.get_rank(ep_group), dist.get_world_size(ep_group))
             self.runner = NativeRunner(self.mw, self.ecfg, nb, self.device)
+            if ep_group is not None:
+                # the most routed rows of one decode-sized layer on one rank: verify rows x top-k
+                self.runner.set_ep_group(ep_group, self._bucket(max_num_seqs) * (self.k + 1) * cfg.top_k)
+                self._ep_dummy = None
             if tp_group is not None:
                 self.runner.set_tp_group(tp_group)
             if pp_group is not None:
@@ -427,7 +437,9 @@ class LLM:
                              callback=callbacks[len(reqs)] if callbacks is not None else None))
         self._between = between_steps
         try:
-            if self.device.type == "cuda":
+            if self.device.type == "cuda" and self._ep_group is not None:
+                self._run_native_ep(reqs)
+            elif self.device.type == "cuda":
                 self._run_native(reqs)
             else:
                 self._run_torch(reqs)
@@ -764,6 +776,95 @@ class LLM:
                 accepted += a
                 lg = dl[i * kp1: i * kp1 + a + 1] if dl is not None else None      # verify rows of this request
                 if self._emit(r, pin_out[i, :a + 1].tolist(), lg):
+                    self._finish_row(r, rows)
+        self.stats = dict(steps=steps, accepted=accepted, decode_s=t_decode, bucket=B)
+
+    def _run_native_ep(self, reqs):
+        """GPU engine loop under data-parallel attention + expert parallelism.  Every rank of
+        the EP group serves its own requests, but every MoE layer is a collective, so the
+        ranks step in lockstep: one small all-reduce per iteration agrees on whether anyone
+        prefills (a rank with nothing to admit prefills a one-token dummy prompt into a
+        private row) and whether anyone decodes (a rank with no live rows replays its step
+        with every row inactive).  All ranks use the bucket of max_num_seqs, so their decode
+        graphs are captured in the same iteration.  Greedy decoding only."""
+        import torch.distributed as dist
+        if any(r.params.temperature > 0 or r.params.processes_logits for r in reqs):
+            raise NotImplementedError("GPU DP + EP decodes greedily (temperature 0, no logits processors)")
+        runner, G = self.runner, self._ep_group
+        B = self._bucket(self.ecfg.max_num_seqs)
+        st = self._state(B)
+        kp1 = self.k + 1
+        pin_active = torch.zeros(B, dtype=torch.int32, pin_memory=True)
+        pin_out = torch.zeros(B, kp1, dtype=torch.int32, pin_memory=True)
+        pin_acc = torch.zeros(B, dtype=torch.int32, pin_memory=True)
+        waiting = deque(reqs)
+        rows: List[Optional[_Req]] = [None] * B
+        bt_host = torch.zeros(B, self.max_blocks, dtype=torch.int32)
+        flag = torch.zeros(3, dtype=torch.int32, device=self.device)
+        steps = accepted = 0
+        t_decode = 0.0
+        if self._ep_dummy is None:      # private row of the dummy prefill: its own state and KV block
+            blocks = self.blocks.allocate("__ep_dummy__", 8)
+            bt = [0] * self.max_blocks
+            bt[0] = blocks[0]
+            self._ep_dummy = (self._DecodeState(1, self.k, self.max_blocks, self.device), bt)
+        while True:
+            free = [i for i, r in enumerate(rows) if r is None]
+            adm = []
+            while waiting and free and self.blocks.can_allocate(
+                    len(waiting[0].prompt) + waiting[0].params.max_tokens + kp1 + 1):
+                r = waiting.popleft()
+                r.row = free.pop(0)
+                rows[r.row] = r
+                blocks = self.blocks.allocate(r.rid, len(r.prompt) + r.params.max_tokens + kp1 + 1)
+                bt_host[r.row].zero_()
+                bt_host[r.row, :len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
+                adm.append(r)
+            flag[0] = 1 if adm else 0
+            flag[1] = 1 if any(r is not None for r in rows) else 0
+            flag[2] = 1 if waiting else 0
+            dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=G)
+            f = flag.tolist()
+            if not (f[0] or f[1]):
+                if f[2]:
+                    raise MemoryError("KV cache too small for the next request")
+                break
+            if f[0]:
+                if adm:
+                    st.block_table.copy_(bt_host, non_blocking=False)
+                    self._set_sampling(st, adm)
+                    self._prefill_rows(adm, [0] * len(adm), False, st, bt_host, rows)
+                else:
+                    dst, dbt = self._ep_dummy
+                    runner.prefill([[1]], [dbt], [0], dst)
+            if not f[1] and not f[0]:
+                continue
+            for i, r in enumerate(rows):
+                pin_active[i] = 1 if r is not None else 0
+            st.set_active(pin_active.to(self.device, non_blocking=True))
+            self._step_sample = False
+            graph = None
+            if self.ecfg.cuda_graphs:
+                graph = runner.graphs.get(B)
+                if graph is None:
+                    graph = runner.capture(st)
+            t0 = time.perf_counter()
+            if graph is not None:
+                graph.replay()
+            else:
+                self._decode_eager(st)
+            pin_out.copy_(st.out_tokens, non_blocking=True)
+            pin_acc.copy_(st.n_acc, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            t_decode += time.perf_counter() - t0
+            runner.check_status("decode step")
+            steps += 1
+            for i, r in enumerate(rows):
+                if r is None:
+                    continue
+                a = int(pin_acc[i])
+                accepted += a
+                if self._emit(r, pin_out[i, :a + 1].tolist()):
                     self._finish_row(r, rows)
         self.stats = dict(steps=steps, accepted=accepted, decode_s=t_decode, bucket=B)
 
