@@ -45,7 +45,10 @@ def main():
     ap.add_argument("--prefill-len", type=int, default=8192)
     ap.add_argument("--streams", type=int, default=32)
     ap.add_argument("--skip-extra", action="store_true", help="skip the 32-stream and prefill measurements")
-    ap.add_argument("--ep", action="store_true", help="N>1: experts partitioned across ranks instead of sharded")
+    ap.add_argument("--ep", action="store_true",
+                    help="data-parallel attention + expert-parallel MoE (BASELINE config 3): every rank serves its "
+                         "own streams, routed experts are partitioned over the ranks and exchanged all-to-all")
+    ap.add_argument("--ep-streams", default="1,4,8,16,32", help="--ep: total concurrent streams to measure")
     args = ap.parse_args()
     if args.impl == "reference":
         return _reference_arm(args)
@@ -68,9 +71,17 @@ def main():
 
     t0 = time.time()
     max_len = max(args.prompt_len + args.steps * 3 + args.warmup * 3 + 64, args.prefill_len + 64)
-    llm = LLM("ds4-flash-shape", device="cuda", num_speculative_tokens=2, max_model_len=max_len,
-              max_num_seqs=args.streams, num_layers=args.layers, seed=0, tensor_parallel_size=world,
-              tp_group=dist.group.WORLD if world > 1 else None, tp_rank=rank, expert_parallel=args.ep and world > 1)
+    if args.ep:
+        if world == 1:
+            dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", local),
+                                    store=dist.HashStore())
+        per_rank = -(-max(int(x) for x in args.ep_streams.split(",")) // world)
+        llm = LLM("ds4-flash-shape", device="cuda", num_speculative_tokens=2, max_model_len=max_len,
+                  max_num_seqs=max(per_rank, 1), num_layers=args.layers, seed=0, ep_group=dist.group.WORLD)
+    else:
+        llm = LLM("ds4-flash-shape", device="cuda", num_speculative_tokens=2, max_model_len=max_len,
+                  max_num_seqs=args.streams, num_layers=args.layers, seed=0, tensor_parallel_size=world,
+                  tp_group=dist.group.WORLD if world > 1 else None, tp_rank=rank)
 
     def maxr(v):   # max over ranks of a time-like value
         if world == 1:
@@ -134,7 +145,9 @@ def main():
     # every step advances the sequence by 1 + accepted drafts
     acc = (int(st.seq_pos[0]) - pos0) / args.steps - 1.0
     tok_per_step = 1.0 + acc
-    value = tok_per_step * 1000.0 / ms
+    # --ep: every rank decodes its own stream (data-parallel attention), so the job's aggregate
+    # is world streams' worth of tokens per step
+    value = tok_per_step * 1000.0 / ms * (world if args.ep else 1)
     llm.blocks.release("bench")
 
     # ---- e2e through LLM.generate (1 stream) -----------------------------------------------
@@ -173,6 +186,22 @@ def main():
         extra[f"decode_{S}_streams_tok_s"] = gen / dec_s
         extra[f"decode_{S}_streams_steps_s"] = stt["steps"] / dec_s
 
+    def ep_streams():
+        # ---- DP + EP serving: S total streams spread over the ranks, aggregate decode --------
+        res = {}
+        for S in [int(x) for x in args.ep_streams.split(",")]:
+            n_loc = S // world + (1 if rank < S % world else 0)
+            ps = [prompt(args.prompt_len) for _ in range(n_loc)]
+            llm.generate([prompt(args.prompt_len) for _ in range(n_loc)], SamplingParams(max_tokens=4, ignore_eos=True))
+            outs = llm.generate(ps, SamplingParams(max_tokens=args.steps + 1, ignore_eos=True))
+            gen = sum(len(o.outputs[0].token_ids) - 1 for o in outs)
+            t = torch.tensor([float(gen)], device="cuda")
+            if world > 1:
+                dist.all_reduce(t)
+            dec = (max(o.metrics["e2e_s"] for o in outs) - min(o.metrics["ttft_s"] for o in outs)) if outs else 0.0
+            res[str(S)] = round(float(t) / maxr(dec), 2)
+        extra["ep_decode_tok_s_by_streams"] = res
+
     def prefill():
         # ---- 8k prefill ----------------------------------------------------------------------
         p8 = prompt(args.prefill_len)
@@ -194,25 +223,29 @@ def main():
         finally:
             llm.blocks.release("pf")
         pf_ms = maxr(min(times))
-        extra["prefill_8k_tok_s"] = args.prefill_len * 1000.0 / pf_ms
+        extra["prefill_8k_tok_s"] = args.prefill_len * 1000.0 / pf_ms * (world if args.ep else 1)
         extra["prefill_8k_ms"] = pf_ms
 
     if not args.skip_extra:
-        secondary(f"decode_{args.streams}_streams", streams)
+        if args.ep:
+            ep_streams()     # collective on every rank: not wrapped (a failure must stop all ranks alike)
+        else:
+            secondary(f"decode_{args.streams}_streams", streams)
         secondary("prefill_8k", prefill)
 
     if rank == 0:
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "higher_is_better": True, "scaling": "strong" if world > 1 and not args.ep else "weak",
             "vs_baseline": round(value / BASELINE.get(args.gpus, 214.0), 3),
             "dtype": "bf16 activations; fp8 e4m3 dense + 2-bit codebook experts (the reference's formats)",
             "data": "synthetic prompts, random-init weights (N(0,0.02)) of the DS4-Flash shape",
             "config": {"model": "ds4-flash-shape (32 layers, hidden 4096, 256 experts top-8, MLA, MTP k=2)",
-                       "global_batch": 1, "seq_len": args.prompt_len, "parallelism": (f"tp{world} (fused peer-memory all-reduce)" if llm.runner.ar is not None
-                                                else f"tp{world} (NCCL all-reduce)") + (" + ep" if args.ep else "")
-                            if world > 1 else "single",
+                       "global_batch": world if args.ep else 1, "seq_len": args.prompt_len,
+                       "parallelism": (f"dp{world} attention + ep{world} experts (peer-memory all-to-all)" if args.ep
+                                       else (f"tp{world} (fused peer-memory all-reduce)" if llm.runner.ar is not None
+                                             else f"tp{world} (NCCL all-reduce)") if world > 1 else "single"),
                        "l2": "inputs larger than L2 (each step streams ~7 GB of weights)",
                        "layers": args.layers or 32},
             "mtp_acceptance_per_step": round(acc, 4), "steps_per_s": round(1000.0 / ms, 2),
@@ -221,7 +254,7 @@ def main():
                     "d2h_bytes_per_step": 4 * (llm.k + 1) + 4},
             "gpu_launches": launches_per_step * args.steps,
             "load_s": round(load_s, 1),
-            **{k: round(v, 2) for k, v in extra.items()},
+            **{k: (round(v, 2) if isinstance(v, float) else v) for k, v in extra.items()},
         }
         if errors:
             out["errors"] = errors
