@@ -305,3 +305,33 @@ def test_chunked_prefill_interleaves_with_decode():
         assert all(d - b <= 8 for _, b, d, _ in log)
         assert sum(1 for c in log if c[3] == 1) >= 5             # chunks that ran beside a decoding row
         assert llm.stats["prefill_chunks"] == len(llm._chunk_log)
+
+
+def test_reference_dsa_selection():
+    """The oracle's DSA indexer: no selection while the context fits in index_topk (the
+    forward equals the dense one); with a small top-k every query keeps exactly top-k keys
+    at or before its position (fewer when fewer exist), and the logits change."""
+    import torch
+    from vllm_moet_b200.config import glm52_config
+    from vllm_moet_b200.models import reference
+    from vllm_moet_b200.models.weights import random_weights
+    cfg = glm52_config(num_layers=2, hidden=256, vocab=512, num_experts=8, moe_intermediate=64,
+                       dense_intermediate=128, num_dense_layers=1, num_heads=4, q_lora_rank=64, top_k=2,
+                       index_heads=4, index_head_dim=32, index_topk=4096)
+    mw = random_weights(cfg, "cpu", seed=3, with_mtp=False)
+    T = 40
+    toks = torch.randint(3, 512, (T,), generator=torch.Generator().manual_seed(1))
+    cs = reference.rope_cos_sin(cfg, 128)
+    dense, _ = reference.forward(mw, toks, torch.arange(T), cs)
+    lw = mw.layers[0]
+    x = torch.randn(T, cfg.hidden)
+    qa = torch.randn(T, cfg.q_lora_rank)
+    assert reference.dsa_select(cfg, lw, x, qa, torch.arange(T)) is None
+    small = cfg.replace(index_topk=8)
+    keep = reference.dsa_select(small, lw, x, qa, torch.arange(T))
+    assert keep.shape == (T, T)
+    # causal keys kept per query: all of them up to 8, then exactly 8 (the attention masks the rest)
+    assert all(int(keep[t, :t + 1].sum()) == min(t + 1, 8) for t in range(T))
+    mw.cfg = small
+    sparse, _ = reference.forward(mw, toks, torch.arange(T), cs)
+    assert not torch.allclose(sparse, dense)

@@ -105,9 +105,11 @@ def test_nvfp4_kv_engine_tracks_bf16_engine(llm):
 
 
 def test_indexer_engine(llm):
-    """DSA indexer + sparse MLA decode: with top-k >= the context the selection is
-    every position, so tokens equal the dense engine's; a small top-k still runs
-    deterministically."""
+    """DSA indexer + sparse MLA: with top-k >= the context the selection is every position,
+    so tokens equal the dense engine's.  With a small top-k the prompt is prefilled in
+    top-k-sized chunks (sparse attention over the paged cache after the first chunk) and
+    decoded sparsely; the emitted tokens track the fp32 oracle with the same DSA selection
+    (teacher-forced), and the run is deterministic."""
     p = [_prompt(45, 21)]
     sp = SamplingParams(max_tokens=8, ignore_eos=True)
     ref = llm.generate(p, sp)[0].outputs[0].token_ids
@@ -115,10 +117,20 @@ def test_indexer_engine(llm):
                max_model_len=1024, max_num_seqs=4)
     assert full.generate(p, sp)[0].outputs[0].token_ids == ref
     del full
-    sparse = LLM(small_cfg().replace(index_heads=8, index_topk=16), device="cuda", num_speculative_tokens=2,
+    sparse = LLM(small_cfg().replace(index_heads=8, index_topk=32), device="cuda", num_speculative_tokens=2,
                  max_model_len=1024, max_num_seqs=4)
+    p = [_prompt(150, 22)]
     a = sparse.generate(p, sp)[0].outputs[0].token_ids
     assert a == sparse.generate(p, sp)[0].outputs[0].token_ids and len(a) == 8
+    assert any(e - s0 < 150 for _, s0, e, _ in sparse._chunk_log)      # the prompt ran in chunks
+    cs = reference.rope_cos_sin(sparse.cfg, 512, "cuda")
+    toks = list(p[0])
+    for i, tok in enumerate(a):
+        lg, _ = reference.forward(sparse.mw, torch.tensor(toks, device="cuda"), torch.arange(len(toks), device="cuda"),
+                                  cs)
+        row = lg[-1]
+        assert float(row[tok]) >= float(row.max()) - 0.5 * (float(row.std()) + 1e-6), (i, tok, int(row.argmax()))
+        toks.append(tok)
 
 
 @pytest.mark.parametrize("tp,ep", [(4, False), (8, False), (8, True)])

@@ -106,6 +106,13 @@ class LLM:
             self._chunk_budget = int(max_num_batched_tokens or 2048)
             if self._chunk_budget < 1:
                 raise ValueError("max_num_batched_tokens must be >= 1")
+        if (self._chunk_budget is None and self.device.type == "cuda" and cfg.index_heads and ep_group is None
+                and sp_group is None and dcp_group is None):
+            # DSA models on the GPU: prompts run in chunks of index_topk tokens.  The first chunk
+            # sees at most index_topk keys per query (dense == sparse); every later chunk runs the
+            # absorbed attention over the paged cache with the indexer's top-k selection per row,
+            # so a long prompt is prefilled with sparse attention and never builds a T x T score
+            self._chunk_budget = int(max_num_batched_tokens or cfg.index_topk)
         if enable_prefix_caching and (sp_group is not None or dcp_group is not None):
             raise ValueError("prefix caching keeps whole per-sequence caches: not with SP prefill / DCP decode")
         if self.device.type == "cuda" and cfg.expert_scale != "ue8m0":

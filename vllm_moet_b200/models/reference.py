@@ -200,17 +200,51 @@ def dense_ffn(cfg: ModelConfig, lw: LayerWeights, h: torch.Tensor) -> torch.Tens
 
 
 class RefKV:
-    """Per-sequence, per-layer cache of (k [Hh, L, qk], v [Hh, L, v]) in fp32."""
+    """Per-sequence, per-layer cache of (k [Hh, L, qk], v [Hh, L, v]) in fp32, and of the
+    DSA indexer keys [L, D] of layers with an indexer."""
 
     def __init__(self, n_layers: int):
         self.k = [None] * n_layers
         self.v = [None] * n_layers
+        self.idx = [None] * n_layers
 
     def truncate(self, length: int):
         for i in range(len(self.k)):
             if self.k[i] is not None:
                 self.k[i] = self.k[i][:, :length]
                 self.v[i] = self.v[i][:, :length]
+            if self.idx[i] is not None:
+                self.idx[i] = self.idx[i][:length]
+
+
+def dsa_select(cfg: ModelConfig, lw: LayerWeights, x: torch.Tensor, qa: torch.Tensor, qpos: torch.Tensor,
+               cache: Optional[RefKV] = None, li: int = 0) -> Optional[torch.Tensor]:
+    """DeepSeek sparse attention ("lightning indexer"): with the normed hidden x [T, H] and
+    normed q_a [T, q_lora], keys k_s = W_k x_s (cached), queries q_t,h = W_q q_a and head
+    weights w_t = W_w x_t give score(t, s) = sum_h w_t,h relu(q_t,h . k_s) over s <= pos(t);
+    each query keeps the index_topk highest (lowest position first among ties).  Returns
+    the [T, L] keep mask, or None while the context fits in index_topk (every key kept)."""
+    if lw.idx_wq is None or not cfg.index_heads:
+        return None
+    T = x.shape[0]
+    Hi, Di = cfg.index_heads, cfg.index_head_dim
+    ki = x.float() @ lw.idx_wk.dequant().t()
+    if cache is not None:
+        if cache.idx[li] is not None:
+            ki = torch.cat([cache.idx[li], ki], dim=0)
+        cache.idx[li] = ki
+    L = ki.shape[0]
+    if L <= cfg.index_topk:
+        return None
+    qi = (qa.float() @ lw.idx_wq.dequant().t()).view(T, Hi, Di)
+    wi = x.float() @ lw.idx_ww.dequant().t()
+    sc = (torch.relu(torch.einsum("thd,sd->ths", qi, ki)) * wi[..., None]).sum(1)      # [T, L]
+    kpos = torch.arange(L, device=x.device)
+    sc = sc.masked_fill(kpos[None, :] > qpos[:, None], float("-inf"))
+    top = _stable_topk(sc, cfg.index_topk)
+    keep = torch.zeros(T, L, dtype=torch.bool, device=x.device)
+    keep.scatter_(1, top, True)
+    return keep
 
 
 def attention(cfg: ModelConfig, lw: LayerWeights, x: torch.Tensor, positions: torch.Tensor, cs: torch.Tensor,
@@ -242,6 +276,9 @@ def attention(cfg: ModelConfig, lw: LayerWeights, x: torch.Tensor, positions: to
     kpos = torch.arange(L, device=x.device)
     qpos = (L - T) + torch.arange(T, device=x.device)
     s = s.masked_fill(kpos[None, None, :] > qpos[None, :, None], float("-inf"))
+    keep = dsa_select(cfg, lw, x, qa, qpos, cache, li)
+    if keep is not None:
+        s = s.masked_fill(~keep[None], float("-inf"))
     o = torch.softmax(s, dim=-1) @ v                       # [Hh, T, vd]
     return o.transpose(0, 1).reshape(T, Hh * vd) @ lw.o.dequant().t()
 
