@@ -117,20 +117,31 @@ def test_indexer_engine(llm):
                max_model_len=1024, max_num_seqs=4)
     assert full.generate(p, sp)[0].outputs[0].token_ids == ref
     del full
-    sparse = LLM(small_cfg().replace(index_heads=8, index_topk=32), device="cuda", num_speculative_tokens=2,
+    # top-k 64 over a 150-token prompt: chunks [0, 64) dense (exact), [64, 128) and [128, 150)
+    # sparse over the paged cache.  The final prefill logits sit at the quantisation floor
+    # from the fp32 oracle with the same DSA selection (0.124 with no sparsity on this
+    # model) and far from the dense oracle; smaller top-k makes the comparison depend on
+    # selection flips of the fp8-quantised indexer inputs near the boundary.
+    sparse = LLM(small_cfg().replace(index_heads=8, index_topk=64), device="cuda", num_speculative_tokens=2,
                  max_model_len=1024, max_num_seqs=4)
     p = [_prompt(150, 22)]
     a = sparse.generate(p, sp)[0].outputs[0].token_ids
-    assert a == sparse.generate(p, sp)[0].outputs[0].token_ids and len(a) == 8
-    assert any(e - s0 < 150 for _, s0, e, _ in sparse._chunk_log)      # the prompt ran in chunks
+    assert [(s0, e) for _, s0, e, _ in sparse._chunk_log] == [(0, 64), (64, 128), (128, 150)]
+    b = sparse.generate(p, SamplingParams(max_tokens=1, ignore_eos=True))[0].outputs[0].token_ids
+    lg = sparse.runner.ws_prefill.bufs[("main.logits", torch.float32)][: sparse.cfg.vocab].clone()
+    assert a == sparse.generate(p, sp)[0].outputs[0].token_ids and len(a) == 8 and b[0] == a[0]
     cs = reference.rope_cos_sin(sparse.cfg, 512, "cuda")
-    toks = list(p[0])
-    for i, tok in enumerate(a):
-        lg, _ = reference.forward(sparse.mw, torch.tensor(toks, device="cuda"), torch.arange(len(toks), device="cuda"),
-                                  cs)
-        row = lg[-1]
-        assert float(row[tok]) >= float(row.max()) - 0.5 * (float(row.std()) + 1e-6), (i, tok, int(row.argmax()))
-        toks.append(tok)
+    t = torch.tensor(p[0], device="cuda")
+    ref_sparse = reference.forward(sparse.mw, t, torch.arange(150, device="cuda"), cs)[0][-1]
+    cfg0 = sparse.mw.cfg
+    sparse.mw.cfg = cfg0.replace(index_topk=4096)
+    try:
+        ref_dense = reference.forward(sparse.mw, t, torch.arange(150, device="cuda"), cs)[0][-1]
+    finally:
+        sparse.mw.cfg = cfg0
+    e_s, e_d = _rel(lg, ref_sparse), _rel(lg, ref_dense)
+    assert e_s < 0.2 and e_s < 0.5 * e_d, (e_s, e_d)
+    assert float(ref_sparse[a[0]]) >= float(ref_sparse.max()) - 0.5 * (float(ref_sparse.std()) + 1e-6)
 
 
 @pytest.mark.parametrize("tp,ep", [(4, False), (8, False), (8, True)])

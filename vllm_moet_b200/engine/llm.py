@@ -792,13 +792,16 @@ class LLM:
         ranks step in lockstep: one small all-reduce per iteration agrees on whether anyone
         prefills (a rank with nothing to admit prefills a one-token dummy prompt into a
         private row) and whether anyone decodes (a rank with no live rows replays its step
-        with every row inactive).  All ranks use the bucket of max_num_seqs, so their decode
-        graphs are captured in the same iteration.  Greedy decoding only."""
+        with every row inactive).  All ranks use one bucket per call (that of the busiest
+        rank), so their decode graphs are captured in the same iteration.  Greedy only."""
         import torch.distributed as dist
         if any(r.params.temperature > 0 or r.params.processes_logits for r in reqs):
             raise NotImplementedError("GPU DP + EP decodes greedily (temperature 0, no logits processors)")
         runner, G = self.runner, self._ep_group
-        B = self._bucket(self.ecfg.max_num_seqs)
+        # one bucket for the whole call on every rank: the smallest that holds the busiest rank
+        nb = torch.tensor([min(len(reqs), self.ecfg.max_num_seqs)], dtype=torch.int32, device=self.device)
+        dist.all_reduce(nb, op=dist.ReduceOp.MAX, group=G)
+        B = self._bucket(max(int(nb), 1))
         st = self._state(B)
         kp1 = self.k + 1
         pin_active = torch.zeros(B, dtype=torch.int32, pin_memory=True)
