@@ -155,71 +155,78 @@ __global__ void __launch_bounds__(gs::kWarps * 32, 1) gemv_stream_kernel(GemvStr
       sas[i] = r < p.T ? ue8m0_to_float(p.sA[(size_t)r * p.sa_stride + c]) : 0.f;
     }
   } else {
-    // fused RMSNorm + quantisation: one thread per (row, 64-group); the rounding
-    // follows rmsnorm_quant (bf16 module output, then e4m3 with a UE8M0 scale)
-    float* ssq = red;                                       // [T][ng] partial sums of squares
-    for (int i = threadIdx.x; i < p.T * ng; i += blockDim.x) {
-      const int r = i / ng, c = i % ng;
+    // fused RMSNorm + quantisation (rounding as rmsnorm_quant: bf16 module output, then
+    // e4m3 with a UE8M0 scale per 64), compact so the code a CTA fetches once stays small:
+    // pass 1 -- per-row sums of squares, one 8-element vector per thread and step;
+    // pass 2 -- 8 consecutive lanes per 64-group: normalise, group amax by shuffles,
+    // scale and convert their 8 elements each.
+    float* ssq = red;                                        // [kMaxT] row sums of squares
+    if (threadIdx.x < kMaxT) ssq[threadIdx.x] = 0.f;
+    __syncthreads();
+    const int vpr = p.K / 8;                                 // 8-element vectors per row
+#pragma unroll 1
+    for (int r = 0; r < p.T; r++) {
       float acc = 0.f;
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
+      for (int i = threadIdx.x; i < vpr; i += blockDim.x) {
         float v[8];
-        gs_load8(p, r, c * 64 + u * 8, v, epoch);
+        gs_load8(p, r, i * 8, v, epoch);
 #pragma unroll
         for (int q = 0; q < 8; q++) acc = fmaf(v[q], v[q], acc);
       }
-      ssq[i] = acc;
+      acc = warp_sum(acc);
+      if (lane == 0) atomicAdd(&ssq[r], acc);
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < kMaxT * ng; i += blockDim.x) {
-      const int r = i / ng, c = i % ng;
-      uint8_t* dst = xs + (size_t)r * KP + c * 64;
-      if (r >= p.T) {
-        for (int b = 0; b < 64; b += 16) *reinterpret_cast<uint4*>(dst + b) = make_uint4(0, 0, 0, 0);
-        sas[i] = 0.f;
-        continue;
-      }
-      float tot = 0.f;
-      for (int q = 0; q < ng; q++) tot += ssq[r * ng + q];
-      const float rinv = rsqrtf(tot / (float)p.K + p.eps);
-      const uint4* gr = reinterpret_cast<const uint4*>(p.gamma + c * 64);
-      float y[64];
+    const int units = p.T * vpr, padded = (units + blockDim.x - 1) / blockDim.x * blockDim.x;
+#pragma unroll 1
+    for (int u = threadIdx.x; u < padded; u += blockDim.x) {
+      const bool live = u < units;
+      const int r = live ? u / vpr : 0, e8 = live ? u - r * vpr : 0;
+      float y[8];
       float amax = 0.f;
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
-        float v[8];
-        gs_load8(p, r, c * 64 + u * 8, v, epoch);
-        if (p.xout && blockIdx.x == 0) {    // the summed residual stream, written once
+      if (live) {
+        gs_load8(p, r, e8 * 8, y, epoch);
+        if (p.xout && blockIdx.x == 0) {       // the summed residual stream, written once
           uint32_t o[4];
 #pragma unroll
           for (int q = 0; q < 4; q++) {
-            const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * q], v[2 * q + 1]);
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(y[2 * q], y[2 * q + 1]);
             o[q] = *reinterpret_cast<const uint32_t*>(&b2);
           }
-          *reinterpret_cast<uint4*>(p.xout + (size_t)r * p.K + c * 64 + u * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(p.xout + (size_t)r * p.K + e8 * 8) = make_uint4(o[0], o[1], o[2], o[3]);
         }
-        const uint4 gv = gr[u];
+        const float rinv = rsqrtf(ssq[r] / (float)p.K + p.eps);
+        const uint4 gv = reinterpret_cast<const uint4*>(p.gamma)[e8];
         const __nv_bfloat162* gg = reinterpret_cast<const __nv_bfloat162*>(&gv);
 #pragma unroll
         for (int q = 0; q < 4; q++) {
           const float2 g2 = __bfloat1622float2(gg[q]);
-          const float a = __bfloat162float(__float2bfloat16(v[2 * q] * rinv * g2.x));
-          const float b = __bfloat162float(__float2bfloat16(v[2 * q + 1] * rinv * g2.y));
-          y[u * 8 + 2 * q] = a; y[u * 8 + 2 * q + 1] = b;
-          amax = fmaxf(amax, fmaxf(fabsf(a), fabsf(b)));
+          y[2 * q] = __bfloat162float(__float2bfloat16(y[2 * q] * rinv * g2.x));
+          y[2 * q + 1] = __bfloat162float(__float2bfloat16(y[2 * q + 1] * rinv * g2.y));
+          amax = fmaxf(amax, fmaxf(fabsf(y[2 * q]), fabsf(y[2 * q + 1])));
         }
       }
-      const uint32_t e = ue8m0_for_amax(amax);
-      const float inv = (e >= 1 && e <= 253) ? __uint_as_float((254u - e) << 23) : 0.f;
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+      if (live) {
+        const uint32_t e = ue8m0_for_amax(amax);
+        const float inv = (e >= 1 && e <= 253) ? __uint_as_float((254u - e) << 23) : 0.f;
+        uint32_t w[2];
 #pragma unroll
-      for (int b = 0; b < 64; b += 16) {
-        uint8_t o[16];
-#pragma unroll
-        for (int q = 0; q < 16; q++) o[q] = f32_to_e4m3(y[b + q] * inv);
-        *reinterpret_cast<uint4*>(dst + b) = *reinterpret_cast<const uint4*>(o);
+        for (int h = 0; h < 2; h++)
+          w[h] = (uint32_t)f32_to_e4m3(y[4 * h] * inv) | ((uint32_t)f32_to_e4m3(y[4 * h + 1] * inv) << 8) |
+                 ((uint32_t)f32_to_e4m3(y[4 * h + 2] * inv) << 16) | ((uint32_t)f32_to_e4m3(y[4 * h + 3] * inv) << 24);
+        *reinterpret_cast<uint2*>(xs + (size_t)r * KP + e8 * 8) = make_uint2(w[0], w[1]);
+        if ((e8 & 7) == 0) sas[r * ng + (e8 >> 3)] = ue8m0_to_float(e);
       }
-      sas[i] = ue8m0_to_float(e);
     }
+    // rows beyond T: zero activations and scales
+    for (int i = threadIdx.x; i < (kMaxT - p.T) * (p.K / 16); i += blockDim.x) {
+      const int r = p.T + i / (p.K / 16), c = (i % (p.K / 16)) * 16;
+      *reinterpret_cast<uint4*>(xs + (size_t)r * KP + c) = make_uint4(0, 0, 0, 0);
+    }
+    for (int i = p.T * ng + threadIdx.x; i < kMaxT * ng; i += blockDim.x) sas[i] = 0.f;
   }
   __syncthreads();
   if (p.ar_consume) ar_consumer_done(p.ar);   // the receive slots are no longer read

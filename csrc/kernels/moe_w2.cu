@@ -51,6 +51,8 @@ struct W2Args {
   // expert parallelism, return leg: output row r (sorted) goes to the source rank's return
   // row ret_rows[r] = src * cap + i (peer store), and the grid publishes a return flag
   int ep_on; const int* ret_rows; EpDesc ep;
+  // K slices (grid.z): slice z covers 64-k chunks [z * cps, (z + 1) * cps) and writes out + z * part_stride
+  int cps; long long part_stride;
 };
 
 // 10-bit quintal word -> (d0 | d2 << 4) | (d1 | d3 << 4) << 8; x / 5 = (x * 0x334) >> 12 for x < 1024
@@ -75,7 +77,7 @@ MOET_DEVICE uint32_t quintal_reg(uint32_t csel, uint32_t Ta, uint32_t Tb, uint32
 // Destination of output row r0 + j: the local out matrix, or under expert parallelism the
 // source rank's return row in peer memory.
 MOET_DEVICE float* w2_out_row(const W2Args& p, int r) {
-  if (!p.ep_on) return p.out + (size_t)r * p.out_stride;
+  if (!p.ep_on) return p.out + (size_t)blockIdx.z * p.part_stride + (size_t)r * p.out_stride;
   const int rr = p.ret_rows[r], src = rr / p.ep.cap;
   return ep_ret(p.ep, src) + (size_t)(rr - src * p.ep.cap) * p.ep.H;
 }
@@ -94,12 +96,13 @@ __device__ __forceinline__ void moe_w2_gemv_body(const W2Args& p) {
   const bool split = p.quintal && slot8 >= 0;                 // refinement over the base: the base must be resident
   const int slot = slot8 >= 0 && !p.quintal ? slot8 : p.slot_table[e];
   if (slot < 0) {
-    if (blockIdx.x == 0 && threadIdx.x == 0 && p.miss_count) atomicAdd(p.miss_count, 1);
+    if (blockIdx.x == 0 && blockIdx.z == 0 && threadIdx.x == 0 && p.miss_count) atomicAdd(p.miss_count, 1);
     for (int j = 0; j < nrows; j++)
       if (lane < 16) w2_out_row(p, r0 + j)[nb * 16 + lane] = 0.f;
     return;
   }
   const int KC = p.K >> 6, KS = p.K >> 5;
+  const int c_begin = blockIdx.z * p.cps, c_end = min(KC, c_begin + p.cps);   // this CTA's K slice
   const bool direct = slot8 >= 0 && !p.quintal;
   const uint8_t* base = direct ? p.pool8 + (size_t)slot8 * p.slot_bytes8 : p.pool + (size_t)slot * p.slot_bytes;
   const uint8_t* codes = direct ? base + p.codes_off8 + (size_t)nb * KC * 1024 + lane * 32
@@ -167,17 +170,17 @@ __device__ __forceinline__ void moe_w2_gemv_body(const W2Args& p) {
   };
   if (direct) {     // delta tier: the A-fragments are stored as e4m3 bytes, no decode
     constexpr int UD = 2;
-    for (int c0 = 0; c0 < KC; c0 += UD) {
+    for (int c0 = c_begin; c0 < c_end; c0 += UD) {
       uint4 w0[UD], w1[UD];
 #pragma unroll
       for (int u = 0; u < UD; u++)
-        if (c0 + u < KC) {
+        if (c0 + u < c_end) {
           w0[u] = ldg_stream_u4(codes + (size_t)(c0 + u) * 1024);
           w1[u] = ldg_stream_u4(codes + (size_t)(c0 + u) * 1024 + 16);
         }
 #pragma unroll
       for (int u = 0; u < UD; u++) {
-        if (c0 + u >= KC) break;
+        if (c0 + u >= c_end) break;
         const uint32_t A0[4] = {w0[u].x, w0[u].y, w0[u].z, w0[u].w};
         const uint32_t A1[4] = {w1[u].x, w1[u].y, w1[u].z, w1[u].w};
         mma_chunk(c0 + u, A0, A1);
@@ -185,19 +188,19 @@ __device__ __forceinline__ void moe_w2_gemv_body(const W2Args& p) {
     }
   } else if (split) {
     constexpr int UQ = 2;
-    for (int c0 = 0; c0 < KC; c0 += UQ) {
+    for (int c0 = c_begin; c0 < c_end; c0 += UQ) {
       uint2 wv[UQ], qv[UQ];
       uint32_t qh[UQ];
 #pragma unroll
       for (int u = 0; u < UQ; u++)
-        if (c0 + u < KC) {
+        if (c0 + u < c_end) {
           wv[u] = ldg_stream_u2(codes + (size_t)(c0 + u) * 256);
           qv[u] = ldg_stream_u2(qrec + (size_t)(c0 + u) * 320 + lane * 8);
           qh[u] = __ldg(reinterpret_cast<const unsigned short*>(qrec + (size_t)(c0 + u) * 320 + 256 + lane * 2));
         }
 #pragma unroll
       for (int u = 0; u < UQ; u++) {
-        if (c0 + u >= KC) break;
+        if (c0 + u >= c_end) break;
         const uint32_t lo = wv[u].x, hi = wv[u].y, r0 = qv[u].x, r1 = qv[u].y, h = qh[u];
         // the lane's 8 ten-bit words (80-bit little-endian record), one per group of 4 codes
         uint32_t T[8];
@@ -221,15 +224,15 @@ __device__ __forceinline__ void moe_w2_gemv_body(const W2Args& p) {
       }
     }
   } else
-  for (int c0 = 0; c0 < KC; c0 += U) {
+  for (int c0 = c_begin; c0 < c_end; c0 += U) {
     uint2 wv[U];
 #pragma unroll
     for (int u = 0; u < U; u++)
-      if (c0 + u < KC) wv[u] = ldg_stream_u2(codes + (size_t)(c0 + u) * 256);
+      if (c0 + u < c_end) wv[u] = ldg_stream_u2(codes + (size_t)(c0 + u) * 256);
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const int c = c0 + u;
-      if (c >= KC) break;
+      if (c >= c_end) break;
       const uint8_t* s = ss + c * 32;
       const float sga = ue8m0_to_float(s[g]), sha = ue8m0_to_float(s[g + 8]);
       const float sgb = ue8m0_to_float(s[16 + g]), shb = ue8m0_to_float(s[24 + g]);
@@ -363,7 +366,9 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
   TORCH_CHECK(K % 64 == 0 && N % 16 == 0, "moe_w2_gemv: N % 16, K % 64");
   TORCH_CHECK(a.stride(1) == 1 && a.size(1) == K, "moe_w2_gemv: A [rows, K] inner-contiguous");
   TORCH_CHECK(sa.is_contiguous() && sa.size(1) == K / 64, "moe_w2_gemv: sA [rows, K/64]");
-  TORCH_CHECK(out.scalar_type() == at::kFloat && out.stride(1) == 1, "moe_w2_gemv: out f32");
+  // out: [rows, N], or [ksplit, rows, N] K-slice partials (the consumers add the slices in order)
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.stride(-1) == 1, "moe_w2_gemv: out f32");
+  const int ksplit = out.dim() == 3 ? out.size(0) : 1;
   TORCH_CHECK(pool.dim() == 2, "moe_w2_gemv: pool [slots, slot_bytes]");
   TORCH_CHECK(codes_off % 16 == 0 && scale_off % 16 == 0 && pool.stride(0) % 16 == 0, "moe_w2_gemv: alignment");
   W2Args p;
@@ -373,7 +378,9 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
   p.pool = (const uint8_t*)pool.data_ptr(); p.slot_bytes = pool.stride(0);
   p.codes_off = codes_off; p.scale_off = scale_off;
   p.slot_table = slot_table.data_ptr<int>();
-  p.out = out.data_ptr<float>(); p.out_stride = out.stride(0);
+  p.out = out.data_ptr<float>(); p.out_stride = out.stride(-2);
+  p.part_stride = out.dim() == 3 ? out.stride(0) : 0;
+  p.cps = (int)((K / 64 + ksplit - 1) / ksplit);
   p.N = N; p.K = K;
   p.miss_count = miss_count.has_value() && miss_count->defined() ? miss_count->data_ptr<int>() : nullptr;
   p.pool8 = nullptr; p.slot_table8 = nullptr; p.slot_bytes8 = p.codes_off8 = p.scale_off8 = 0;
@@ -396,7 +403,8 @@ void moe_w2_gemv(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor>
   }
   const int max_pairs = pairs.size(0);
   const int wpc = 4;
-  dim3 grid((N / 16 + wpc - 1) / wpc, max_pairs);
+  TORCH_CHECK(!p.ep_on || ksplit == 1, "moe_w2_gemv: the EP return leg takes no K slices");
+  dim3 grid((N / 16 + wpc - 1) / wpc, max_pairs, ksplit);
   auto stream = at::cuda::getCurrentCUDAStream();
   // scale stage per warp; split FP4 adds a 640-entry u16 digit table per warp
   const size_t smem = (size_t)wpc * 16 * (K / 32) + (p.quintal ? (size_t)wpc * 640 * 2 : 0);

@@ -163,6 +163,13 @@ def test_moe_w2_gemv(C, T, k, E, N, K, MB):
             ref = A[t] @ W.t()
             assert rel(out[posof_c[t * k + j]].cpu(), ref) < 1e-4, (t, j)
     assert int(miss) == 0
+    # K slices (grid.z): the slices summed in order equal the whole-K GEMV
+    for ks in (2, 3, K // 64 + 1):
+        part = torch.full((ks, R, N), float("nan"), device=DEV)
+        C.moe_w2_gemv(dev(qw2), dev(s), stok, pairs, npairs, dev(pool), 0, N * K // 4, slot_table, part, N, K, MB,
+                      miss)
+        assert torch.allclose(part.sum(0), out, rtol=1e-5, atol=1e-4), ks
+    assert int(miss) == 0
     # a missing expert writes zeros and counts a miss
     slot_table[int(ids[0, 0])] = -1
     C.moe_w2_gemv(dev(qw2), dev(s), stok, pairs, npairs, dev(pool), 0, N * K // 4, slot_table, out, N, K, MB, miss)

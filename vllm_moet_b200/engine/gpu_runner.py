@@ -145,6 +145,8 @@ class NativeRunner:
         # per K slice of the tcgen05 kernel
         self.w2_decode = os.environ.get("MOET_W2_DECODE", "legacy")
         self.w2_tcd_spt = int(os.environ.get("MOET_W2_TCD_SPT", "8"))
+        # K-split the mma.sync decode expert GEMV when its grid is small (MOET_W2_KSPLIT=0: off)
+        self.w2_ksplit = os.environ.get("MOET_W2_KSPLIT", "1") != "0"
 
     # ------------------------------------------------------------------ helpers
     @staticmethod
@@ -265,7 +267,7 @@ class NativeRunner:
         nrows = self.ws.get("ep.nrows", (1,), torch.int32)
         C.ep_dispatch(ep.desc, h2q, h2s, ids)
         C.ep_recv_pairs(ep.desc, MB, idr, rank, stok, posof, pairs, npairs, nrows)
-        c13 = self.ws.get("ep.c13", (R, 2 * I), torch.float32)
+        c13 = self.ws.get("ep.c13", (self._w2_ksplit(2 * I, H, cfg.top_k * ep.world), R, 2 * I), torch.float32)
         C.moe_w2_gemv(ep.rx, ep.rs, stok, pairs, npairs, ex.pool, L.off_codes13, L.off_sc13, ex.slot_table, c13,
                       2 * I, H, MB, self.miss)
         a2q, a2s = self._fp8("ep.a2", R, I)
@@ -709,15 +711,29 @@ class NativeRunner:
             a2q, a2s = self._fp8("a2", R, I)
             C.swiglu_quant(c13, cfg.swiglu_limit or 0.0, None, 1, a2q, a2s)
             return gemv(a2q, a2s, None, L.off_codes2, L.off_sc2, H, I, "y2s")
-        c13 = self.ws.get("c13", (R, 2 * I), torch.float32)
+        P = pairs.shape[0]
+        ks13, ks2 = self._w2_ksplit(2 * I, H, min(P, R)), self._w2_ksplit(H, I, min(P, R))
+        c13 = self.ws.get("c13", (ks13, R, 2 * I), torch.float32)
         C.moe_w2_gemv(h2q, h2s, stok, pairs, npairs, ex.pool, L.off_codes13, L.off_sc13, ex.slot_table, c13,
                       2 * I, H, MB, self.miss, **d13)
         a2q, a2s = self._fp8("a2", R, I)
         C.swiglu_quant(c13, cfg.swiglu_limit or 0.0, None, 1, a2q, a2s)
-        y2 = self.ws.get("y2", (R, H), torch.float32)
+        y2 = self.ws.get("y2", (ks2, R, H), torch.float32)
         C.moe_w2_gemv(a2q, a2s, None, pairs, npairs, ex.pool, L.off_codes2, L.off_sc2, ex.slot_table, y2,
                       H, I, MB, self.miss, **d2)
         return y2
+
+    def _w2_ksplit(self, N: int, K: int, pairs: int) -> int:
+        """K slices of a decode expert GEMV when its grid holds less than one wave of resident
+        warps (16-row blocks x pairs < 148 SMs x 32): small expert shards (TP) otherwise leave
+        each warp a long serial K loop on a nearly empty GPU.  At least 4 64-k chunks per
+        slice.  Measured on the DS4 shape: TP8 w13 30 -> 11 us; one GPU (already one wave)
+        keeps a single slice, where splitting cost 3 us plus the consumers' slice sums."""
+        if not self.w2_ksplit:
+            return 1
+        warps = max(1, (N // 16) * max(pairs, 1))
+        want = (148 * 32) // warps
+        return max(1, min(want, (K // 64) // 4, 16))
 
     def _check(self, name, t):
         """Debug aid (MOET_DEBUG_FINITE=1, eager only): raise at the first non-finite stage output."""

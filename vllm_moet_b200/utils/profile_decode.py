@@ -19,13 +19,16 @@ def main(argv=None):
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--reps", type=int, default=1)
     ap.add_argument("--prompt-len", type=int, default=1024)
+    ap.add_argument("--tp", type=int, default=1,
+                    help="run rank 0's shards of a TP-N model on this GPU without a group (kernel shapes and "
+                         "costs of TP-N; partial sums are not reduced, no collectives)")
     ap.add_argument("--mode", choices=["decode", "prefill"], default="decode",
                     help="profile the captured decode step, or one prefill of --prompt-len tokens")
     a = ap.parse_args(argv)
     from ..engine.llm import LLM
     B = a.batch
     llm = LLM("ds4-flash-shape", device="cuda", num_speculative_tokens=2, max_model_len=a.prompt_len + 256,
-              max_num_seqs=B, num_layers=a.layers)
+              max_num_seqs=B, num_layers=a.layers, tensor_parallel_size=a.tp, tp_rank=0)
     r = llm.runner
     st = llm._state(B)
     g = torch.Generator().manual_seed(0)
