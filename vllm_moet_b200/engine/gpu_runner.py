@@ -727,8 +727,9 @@ class NativeRunner:
         """K slices of a decode expert GEMV when its grid holds less than one wave of resident
         warps (16-row blocks x pairs < 148 SMs x 32): small expert shards (TP) otherwise leave
         each warp a long serial K loop on a nearly empty GPU.  At least 4 64-k chunks per
-        slice.  Measured on the DS4 shape: TP8 w13 30 -> 11 us; one GPU (already one wave)
-        keeps a single slice, where splitting cost 3 us plus the consumers' slice sums."""
+        slice.  Measured on the DS4 shape: rank 0's TP8 decode step (no collectives) 3.99 ->
+        3.77 ms; one GPU (already one wave) keeps a single slice, where splitting cost ~3 us
+        per expert GEMV plus the consumers' slice sums."""
         if not self.w2_ksplit:
             return 1
         warps = max(1, (N // 16) * max(pairs, 1))
