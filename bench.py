@@ -49,6 +49,12 @@ def main():
                     help="data-parallel attention + expert-parallel MoE (BASELINE config 3): every rank serves its "
                          "own streams, routed experts are partitioned over the ranks and exchanged all-to-all")
     ap.add_argument("--ep-streams", default="1,4,8,16,32", help="--ep: total concurrent streams to measure")
+    ap.add_argument("--expert-cache-gb", type=float, default=0.0,
+                    help="residency: serve routed experts from a GPU cache of this many GiB over a host store "
+                         "(reports 1-stream decode through LLM.generate, host fetches included)")
+    ap.add_argument("--expert-store", default="pinned", choices=["pinned", "pack", "tiered"])
+    ap.add_argument("--delta-slots", type=int, default=0, help="residency: FP4 delta-tier slots")
+    ap.add_argument("--gate", action="store_true", help="residency: confidence gate on the delta tier")
     args = ap.parse_args()
     if args.impl == "reference":
         return _reference_arm(args)
@@ -78,6 +84,8 @@ def main():
         per_rank = -(-max(int(x) for x in args.ep_streams.split(",")) // world)
         llm = LLM("ds4-flash-shape", device="cuda", num_speculative_tokens=2, max_model_len=max_len,
                   max_num_seqs=max(per_rank, 1), num_layers=args.layers, seed=0, ep_group=dist.group.WORLD)
+    elif args.expert_cache_gb > 0 or args.delta_slots > 0:
+        return _residency(args, world, rank, local)
     else:
         llm = LLM("ds4-flash-shape", device="cuda", num_speculative_tokens=2, max_model_len=max_len,
                   max_num_seqs=args.streams, num_layers=args.layers, seed=0, tensor_parallel_size=world,
@@ -268,6 +276,55 @@ def main():
         sys.stdout.flush()
         sys.stderr.flush()
         os._exit(0)
+    return 0
+
+
+def _residency(args, world, rank, local):
+    """Residency tiers on the DS4 shape: routed experts served from a GPU expert cache
+    (misses fetched from the pinned / pack / tiered host store and the step replayed) and/or
+    the FP4 delta tier (with the confidence gate).  Decode runs through LLM.generate with
+    one stream; the rate is host wall clock from the first token to completion (fetches,
+    replays and promotions included), the device graph replays in between."""
+    import tempfile
+
+    import torch
+    from vllm_moet_b200 import LLM, SamplingParams
+    from vllm_moet_b200.models.weights import ExpertLayout
+    from vllm_moet_b200.config import get_preset
+    if world > 1:
+        raise SystemExit("residency bench: one GPU")
+    cfg = get_preset("ds4-flash-shape")
+    slot_b = ExpertLayout(H=cfg.hidden, I=cfg.moe_intermediate).slot_bytes
+    slots = int(args.expert_cache_gb * (1 << 30) // slot_b)
+    store_dir = tempfile.mkdtemp(prefix="moet-pack-") if args.expert_store != "pinned" else None
+    t0 = time.time()
+    llm = LLM("ds4-flash-shape", device="cuda", num_speculative_tokens=2, max_model_len=args.prompt_len + 4096,
+              max_num_seqs=1, num_layers=args.layers, seed=0, expert_cache_slots=slots,
+              expert_store=args.expert_store, expert_store_dir=store_dir, delta_slots=args.delta_slots,
+              gate=args.gate if args.delta_slots else None)
+    load_s = time.time() - t0
+    g = torch.Generator().manual_seed(1234)
+    prompt = lambda n: torch.randint(3, llm.cfg.vocab, (n,), generator=g).tolist()   # noqa: E731
+    for _ in range(args.warmup):
+        llm.generate([prompt(args.prompt_len)], SamplingParams(max_tokens=8, ignore_eos=True))
+    outs = llm.generate([prompt(args.prompt_len)], SamplingParams(max_tokens=args.steps + 1, ignore_eos=True))
+    m = outs[0].metrics
+    n = len(outs[0].outputs[0].token_ids) - 1
+    rate = n / (m["e2e_s"] - m["ttft_s"])
+    n_moe = sum(1 for lw in llm.mw.layers if lw.is_moe) + (1 if llm.mw.mtp is not None else 0)
+    out = {"metric": METRIC + " [residency tiers]", "value": round(rate, 2), "unit": "tok/s", "n_gpus": 1,
+           "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "bf16 activations; fp8 dense; 2-bit experts (+ FP4 delta tier)",
+           "data": "synthetic prompts, random-init weights of the DS4-Flash shape",
+           "config": {"model": "ds4-flash-shape (32 layers, 256 experts top-8, MTP k=2)", "global_batch": 1,
+                      "seq_len": args.prompt_len, "parallelism": "single",
+                      "expert_cache_gb": args.expert_cache_gb, "expert_cache_slots": slots,
+                      "expert_slots_total": n_moe * cfg.num_experts, "expert_store": args.expert_store,
+                      "delta_slots": args.delta_slots, "gate": bool(args.gate)},
+           "stats": {k: v for k, v in llm.stats.items() if isinstance(v, (int, float))},
+           "cache": dict(llm.cache.stats) if getattr(llm, "cache", None) is not None else None,
+           "load_s": round(load_s, 1)}
+    print(json.dumps(out, default=str), flush=True)
     return 0
 
 

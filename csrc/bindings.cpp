@@ -52,6 +52,8 @@ void ep_recv_pairs(torch::Tensor desc, int64_t MB, torch::Tensor ids, torch::Ten
                    torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
                    torch::Tensor n_rows);
 int64_t ep_buffer_bytes(int64_t world, int64_t cap, int64_t H);
+void experts_quant_pack(torch::Tensor w, torch::Tensor ts, torch::Tensor packed, torch::Tensor sf,
+                        torch::Tensor counters, torch::Tensor pool, int64_t off_c, int64_t off_s, int64_t zero_mode);
 void moe_w2_tcd(torch::Tensor a, torch::Tensor sa, c10::optional<torch::Tensor> gather, torch::Tensor pairs,
                 torch::Tensor n_pairs, torch::Tensor pool, int64_t codes_off, int64_t scale_off,
                 torch::Tensor slot_table, torch::Tensor out, int64_t N, int64_t K, int64_t rows_per_pair,
@@ -171,6 +173,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("slot_table8") = py::none(), py::arg("quintal") = false, py::arg("ep") = py::none(),
         py::arg("ret_rows") = py::none());
   m.def("moe_w2_tcd", &moe_w2_tcd);
+  m.def("experts_quant_pack", &experts_quant_pack);
   m.def("ep_dispatch", &ep_dispatch);
   m.def("ep_recv_pairs", &ep_recv_pairs);
   m.def("ep_buffer_bytes", &ep_buffer_bytes);

@@ -15,9 +15,8 @@
 namespace moet {
 
 // one thread per (row, 16-block)
-__global__ void nvfp4_quant_kernel(const float* __restrict__ w, int N, int K, float ts,
-                                   uint8_t* __restrict__ packed, uint8_t* __restrict__ sf) {
-  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+MOET_DEVICE void nvfp4_quant_body(long long idx, const float* __restrict__ w, int N, int K, float ts,
+                                  uint8_t* __restrict__ packed, uint8_t* __restrict__ sf) {
   const long long nblk = (long long)N * (K / 16);
   if (idx >= nblk) return;
   const int r = idx / (K / 16), b = idx % (K / 16);
@@ -41,14 +40,26 @@ __global__ void nvfp4_quant_kernel(const float* __restrict__ w, int N, int K, fl
   sf[(size_t)r * (K / 16) + b] = sq;
 }
 
+__global__ void nvfp4_quant_kernel(const float* __restrict__ w, int N, int K, float ts,
+                                   uint8_t* __restrict__ packed, uint8_t* __restrict__ sf) {
+  nvfp4_quant_body((long long)blockIdx.x * blockDim.x + threadIdx.x, w, N, K, ts, packed, sf);
+}
+
+// batched over experts (blockIdx.y), per-expert tensor scale ts[e]
+__global__ void nvfp4_quant_batched_kernel(const float* __restrict__ w, int N, int K, const double* __restrict__ ts,
+                                           uint8_t* __restrict__ packed, uint8_t* __restrict__ sf) {
+  const size_t e = blockIdx.y;
+  nvfp4_quant_body((long long)blockIdx.x * blockDim.x + threadIdx.x, w + e * N * K, N, K, (float)ts[e],
+                   packed + e * N * (K / 2), sf + e * N * (K / 16));
+}
+
 __constant__ double kE2M1Val[8] = {0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0};
 
 // one thread per (row, 32-block)
-__global__ void w2_quant_pack_kernel(const uint8_t* __restrict__ packed, const uint8_t* __restrict__ sf, double ts,
-                                     int N, int K, int zero_mode, uint8_t* __restrict__ codes_plane,
-                                     uint8_t* __restrict__ scale_plane, uint8_t* __restrict__ fp4_plane,
-                                     unsigned long long* __restrict__ counters) {
-  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+MOET_DEVICE void w2_quant_pack_body(long long idx, const uint8_t* __restrict__ packed, const uint8_t* __restrict__ sf,
+                                    double ts, int N, int K, int zero_mode, uint8_t* __restrict__ codes_plane,
+                                    uint8_t* __restrict__ scale_plane, uint8_t* __restrict__ fp4_plane,
+                                    unsigned long long* __restrict__ counters) {
   const int KS = K / 32, KC = K / 64;
   if (idx >= (long long)N * KS) return;
   const int r = idx / KS, ks = idx % KS;
@@ -113,6 +124,36 @@ __global__ void w2_quant_pack_kernel(const uint8_t* __restrict__ packed, const u
   if (counters && nzero) { atomicAdd(&counters[0], nzero); atomicAdd(&counters[1], nneg); }
 }
 
+__global__ void w2_quant_pack_kernel(const uint8_t* __restrict__ packed, const uint8_t* __restrict__ sf, double ts,
+                                     int N, int K, int zero_mode, uint8_t* __restrict__ codes_plane,
+                                     uint8_t* __restrict__ scale_plane, uint8_t* __restrict__ fp4_plane,
+                                     unsigned long long* __restrict__ counters) {
+  w2_quant_pack_body((long long)blockIdx.x * blockDim.x + threadIdx.x, packed, sf, ts, N, K, zero_mode, codes_plane,
+                     scale_plane, fp4_plane, counters);
+}
+
+// Batched over experts (blockIdx.y) into slot rows of a pool.  zero_mode 0 / 1 as above and
+// counting zeros per expert; zero_mode 2 is the second pass of the "auto" rule: an expert whose
+// counters show a sign-unbalanced set of exact zeros (the minority sign under 5 %) is packed
+// again with mode 1, every other expert is left as it is -- no host round trip.
+__global__ void w2_quant_pack_batched_kernel(const uint8_t* __restrict__ packed, const uint8_t* __restrict__ sf,
+                                             const double* __restrict__ ts, int N, int K, int zero_mode,
+                                             uint8_t* __restrict__ pool, long long slot_stride, long long off_c,
+                                             long long off_s, unsigned long long* __restrict__ counters) {
+  const size_t e = blockIdx.y;
+  unsigned long long* cnt = counters + 2 * e;
+  int mode = zero_mode;
+  if (zero_mode == 2) {
+    const unsigned long long nz = cnt[0], nneg = cnt[1];
+    if (!(nz && (double)min(nneg, nz - nneg) < 0.05 * (double)nz)) return;
+    mode = 1;
+  }
+  uint8_t* slot = pool + e * slot_stride;
+  w2_quant_pack_body((long long)blockIdx.x * blockDim.x + threadIdx.x, packed + e * N * (K / 2),
+                     sf + e * N * (K / 16), ts[e], N, K, mode, slot + off_c, slot + off_s, nullptr,
+                     zero_mode == 2 ? nullptr : cnt);
+}
+
 }  // namespace moet
 
 using namespace moet;
@@ -141,5 +182,32 @@ void w2_quant_pack(torch::Tensor packed, torch::Tensor sf, double ts, int64_t ze
       (const uint8_t*)packed.data_ptr(), (const uint8_t*)sf.data_ptr(), ts, N, K, (int)zero_mode,
       (uint8_t*)codes_plane.data_ptr(), (uint8_t*)scale_plane.data_ptr(), (uint8_t*)opt_ptr(fp4_plane),
       (unsigned long long*)opt_ptr(counters));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// All experts of a chunk in three launches: w [n, N, K] f32 (cuda), ts [n] f64 (the
+// per-expert tensor scales), scratch packed [n, N, K/2] / sf [n, N, K/16] u8, counters
+// [n, 2] u64 zeroed, slot rows pool [n, slot_stride] (codes at off_c, scales at off_s).
+void experts_quant_pack(torch::Tensor w, torch::Tensor ts, torch::Tensor packed, torch::Tensor sf,
+                        torch::Tensor counters, torch::Tensor pool, int64_t off_c, int64_t off_s, int64_t zero_mode) {
+  const int n = w.size(0), N = w.size(1), K = w.size(2);
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && K % 64 == 0 && N % 16 == 0,
+              "experts_quant_pack: w f32 [n, N, K], N % 16, K % 64");
+  TORCH_CHECK(ts.scalar_type() == at::kDouble && ts.numel() == n && counters.numel() >= 2 * n &&
+              packed.numel() >= (int64_t)n * N * K / 2 && sf.numel() >= (int64_t)n * N * K / 16 &&
+              pool.dim() == 2 && pool.size(0) >= n, "experts_quant_pack: shapes");
+  if (n == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const long long nq = (long long)N * (K / 16), np = (long long)N * (K / 32);
+  nvfp4_quant_batched_kernel<<<dim3((nq + 255) / 256, n), 256, 0, stream>>>(
+      w.data_ptr<float>(), N, K, ts.data_ptr<double>(), (uint8_t*)packed.data_ptr(), (uint8_t*)sf.data_ptr());
+  const int first = zero_mode == 1 ? 1 : 0;
+  w2_quant_pack_batched_kernel<<<dim3((np + 127) / 128, n), 128, 0, stream>>>(
+      (const uint8_t*)packed.data_ptr(), (const uint8_t*)sf.data_ptr(), ts.data_ptr<double>(), N, K, first,
+      (uint8_t*)pool.data_ptr(), pool.stride(0), off_c, off_s, (unsigned long long*)counters.data_ptr());
+  if (zero_mode == 2)    // "auto"
+    w2_quant_pack_batched_kernel<<<dim3((np + 127) / 128, n), 128, 0, stream>>>(
+        (const uint8_t*)packed.data_ptr(), (const uint8_t*)sf.data_ptr(), ts.data_ptr<double>(), N, K, 2,
+        (uint8_t*)pool.data_ptr(), pool.stride(0), off_c, off_s, (unsigned long long*)counters.data_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

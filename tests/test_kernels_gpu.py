@@ -409,6 +409,28 @@ def test_w2_quant_pack_matches_golden(C):
     assert torch.equal(fp.cpu(), planes.pack_fp4(nib))
 
 
+@pytest.mark.parametrize("zero_mode", ["auto", "sign", "alt"])
+def test_batched_expert_quant_matches_golden(C, zero_mode):
+    """The batched load-time quantiser (all experts of a chunk per launch, per-expert tensor
+    scales and the zero-sign auto rule on the device) is byte-equal to the golden CPU
+    pipeline, slot by slot; expert 1 has many exact zeros of one sign (auto -> alternate)."""
+    from vllm_moet_b200.models.weights import ExpertLayout, quantize_experts_cpu, quantize_experts_gpu
+    g = torch.Generator().manual_seed(9)
+    n, H, I = 4, 256, 128
+    w13 = torch.randn(n, 2 * I, H, generator=g) * 0.02
+    w2 = torch.randn(n, H, I, generator=g) * 0.02
+    w13[1, :, ::3] = 0.0
+    w2[1, ::2, :] = 0.0
+    w13[2] = 0.0                     # an all-zero matrix: tensor scale 1
+    lay = ExpertLayout(H=H, I=I)
+    ref = torch.zeros(n, lay.slot_bytes, dtype=torch.uint8)
+    quantize_experts_cpu(w13, w2, lay, ref, zero_mode=zero_mode)
+    got = torch.zeros(n, lay.slot_bytes, dtype=torch.uint8, device=DEV)
+    quantize_experts_gpu(w13.to(DEV), w2.to(DEV), lay, got, zero_mode=zero_mode)
+    for e in range(n):
+        assert torch.equal(got[e].cpu(), ref[e]), e
+
+
 def test_argmax_lse(C):
     g = torch.Generator().manual_seed(0)
     x = torch.randn(6, 129280, generator=g)

@@ -91,8 +91,10 @@ def test_decode_tracks_reference_greedy(llm):
 
 
 def test_nvfp4_kv_engine_tracks_bf16_engine(llm):
-    """The same model with a 352 B/token NVFP4 latent cache: prefill logits equal
-    (the cache is not read in prefill) and the decode stays deterministic."""
+    """The same model with a 352 B/token NVFP4 latent cache: prefill logits equal (the cache
+    is not read in prefill); every decode step reads the NVFP4 cache, and its verify-row
+    logits, teacher-forced on the bf16-cache engine's own tokens, stay close to the bf16
+    engine's (NVFP4 KV error only); the decode is deterministic."""
     nv = LLM(small_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=1024, max_num_seqs=4,
              kv_cache_dtype="nvfp4")
     p = [_prompt(40, 11)]
@@ -102,6 +104,17 @@ def test_nvfp4_kv_engine_tracks_bf16_engine(llm):
     ref = llm.generate(p, sp)[0].outputs[0].token_ids
     assert a == b and len(a) == 10
     assert a[0] == ref[0]
+    # teacher-forced decode logits: both engines prefill the same prompt + ref prefix, then one
+    # decode step reads the whole latent cache (bf16 rows vs 352-byte NVFP4 rows)
+    one = SamplingParams(max_tokens=2, ignore_eos=True)
+    errs = []
+    for n in (0, 4, 8):
+        q = [p[0] + ref[:n]]
+        nv.generate(q, one)
+        llm.generate(q, one)
+        lg_nv, lg_bf = nv.runner.main_logits(1)[0].clone(), llm.runner.main_logits(1)[0].clone()
+        errs.append(_rel(lg_nv, lg_bf))
+    assert max(errs) < 0.1, errs
 
 
 def test_indexer_engine(llm):

@@ -119,6 +119,7 @@ class NativeRunner:
         self.cache = None         # residency.ExpertCache when routed experts are served from a host store
         self.delta = None         # residency.DeltaTier (FP4 hot experts) when enabled
         self._moe_index = {}
+        self._route_tag = ""      # routing-buffer suffix of the current MTP draft pass
         self._pend = None         # (residual, out) of a pushed reduction the next RMSNorm completes
         self._pend_add = None     # (residual, reduced partial, out): decode residual add left to the next norm
         self._decode = False
@@ -338,9 +339,16 @@ class NativeRunner:
         return b[: B * (self.k + 1) * V].view(B * (self.k + 1), V)
 
     def route_ids(self, B: int):
-        """Per-MoE-layer routed expert ids of the last decode step of bucket B."""
+        """Per-MoE-layer routed expert ids of the last decode step of bucket B (the MTP layer's
+        draft passes concatenated)."""
         ws = self._bucket_ws(B)
-        return [ws.bufs.get((f"topk_ids.{i}", torch.int32)) for i in range(len(self._moe_index))]
+        out = []
+        for i in range(len(self._moe_index)):
+            parts = [ws.bufs.get((f"topk_ids.{i}", torch.int32))]
+            parts += [ws.bufs.get((f"topk_ids.{i}.p{j}", torch.int32)) for j in range(1, max(self.k, 1))]
+            parts = [t.reshape(-1) for t in parts if t is not None]
+            out.append(torch.cat(parts) if len(parts) > 1 else (parts[0] if parts else None))
+        return out
 
     def _ensure_experts(self, li, ids):
         """Eager passes (prefill, un-captured decode): fetch this layer's routed experts now."""
@@ -558,7 +566,9 @@ class NativeRunner:
         E, k = cfg.num_experts, cfg.top_k
         logits = self.ws.get("rlogits", (T, E), torch.float32)
         mli = self._moe_index.get(id(lw))
-        ids = self.ws.get("topk_ids" if mli is None else f"topk_ids.{mli}", (T, k), torch.int32)
+        # per MoE layer (and per MTP draft pass: the MTP layer runs k times a step) its own
+        # routing buffer, so the replay engine sees every expert the step routed to
+        ids = self.ws.get("topk_ids" if mli is None else f"topk_ids.{mli}{self._route_tag}", (T, k), torch.int32)
         wts = self.ws.get("topk_w", (T, k), torch.float32)
         R = T * k
         ex = lw.experts
@@ -1030,6 +1040,7 @@ class NativeRunner:
         st.drafts[:, 0] = prev_tok
         h_prev = mh[sel]
         for j in range(1, k):
+            self._route_tag = f".p{j}"
             p2 = st.seq_pos + st.n_acc + j
             blk2 = st.block_table.gather(1, (p2 // KV_BLOCK).long().view(B, 1)).view(-1)
             slot2 = blk2.long() * KV_BLOCK + (p2 % KV_BLOCK).long()
@@ -1041,6 +1052,7 @@ class NativeRunner:
             self._argmax(lg, dj)
             st.drafts[:, j] = dj
             prev_tok = dj
+        self._route_tag = ""
         C.mtp_finalize(st.targets, st.n_acc, st.drafts, st.tokens, st.seq_pos, st.active)
         self._pp_broadcast_state(st)
 

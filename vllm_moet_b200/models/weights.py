@@ -269,28 +269,24 @@ class _Rng:
 def quantize_experts_gpu(w13: torch.Tensor, w2: torch.Tensor, layout: ExpertLayout, out_pool: torch.Tensor,
                          zero_mode: str = "auto"):
     """Random-init float experts [n, 2I, H], [n, H, I] (cuda) -> 2-bit slots in out_pool [n, slot_bytes]
-    via NVFP4 (kernel) then the 2-bit requant+pack kernel."""
+    via NVFP4 then the 2-bit requant+pack, all n experts per matrix in three kernel launches
+    (per-expert tensor scales and the zero-sign "auto" rule stay on the device, no host sync)."""
     from ..ops import native
     C = native()
     n = w13.shape[0]
-    for e in range(n):
-        for (mat, off_c, off_s) in ((w13[e], layout.off_codes13, layout.off_sc13),
-                                    (w2[e], layout.off_codes2, layout.off_sc2)):
-            N, K = mat.shape
-            ts = float(mat.abs().max()) / (6.0 * 448.0) or 1.0
-            packed = torch.empty(N, K // 2, dtype=torch.uint8, device=mat.device)
-            sf = torch.empty(N, K // 16, dtype=torch.uint8, device=mat.device)
-            C.nvfp4_quant(mat.contiguous(), ts, packed, sf)
-            nc, ns = N * K // 4, N * K // 32
-            counters = torch.zeros(2, dtype=torch.int64, device=mat.device)
-            mode = 1 if zero_mode == "alt" else 0
-            C.w2_quant_pack(packed, sf, ts, mode, out_pool[e, off_c:off_c + nc], out_pool[e, off_s:off_s + ns],
-                            None, counters)
-            if zero_mode == "auto":
-                nz, nneg = (int(v) for v in counters.tolist())
-                if nz and min(nneg, nz - nneg) < 0.05 * nz:
-                    C.w2_quant_pack(packed, sf, ts, 1, out_pool[e, off_c:off_c + nc],
-                                    out_pool[e, off_s:off_s + ns], None, None)
+    if n == 0:
+        return
+    mode = {"sign": 0, "alt": 1, "auto": 2}[zero_mode]
+    for mat, off_c, off_s in ((w13, layout.off_codes13, layout.off_sc13), (w2, layout.off_codes2, layout.off_sc2)):
+        mat = mat.contiguous()
+        _, N, K = mat.shape
+        # the host rule float(max|w|) / (6 * 448), 1.0 for an all-zero matrix, in double
+        amax = mat.abs().amax(dim=(1, 2)).double()
+        ts = torch.where(amax > 0, amax / (6.0 * 448.0), torch.ones_like(amax))
+        packed = torch.empty(n, N, K // 2, dtype=torch.uint8, device=mat.device)
+        sf = torch.empty(n, N, K // 16, dtype=torch.uint8, device=mat.device)
+        counters = torch.zeros(n, 2, dtype=torch.int64, device=mat.device)
+        C.experts_quant_pack(mat, ts, packed, sf, counters, out_pool, off_c, off_s, mode)
 
 
 def quantize_experts_cpu(w13: torch.Tensor, w2: torch.Tensor, layout: ExpertLayout, out_pool: torch.Tensor,
