@@ -235,6 +235,11 @@ class MoetConfig:
     delta_capture: Optional[str] = None  # .npy of per-step routed expert ids
     gate_fire_timing: bool = False      # promote / replay milliseconds per gate iteration
     gate_dump: Optional[str] = None     # JSONL: one row per gate evaluation
+    # bf12: lossless 12-bit container for dense BF16 linears, converted after load
+    bf12: bool = False
+    bf12_min_numel: int = 1 << 20
+    bf12_verify: bool = True
+    bf12_exclude: str = ""              # comma-separated name substrings kept in BF16
 
     ENV_ALIASES = {
         "prefill_t": "VLLM_MOE_W2_PREFILL_T",
@@ -273,6 +278,10 @@ class MoetConfig:
         "delta_capture": "VLLM_MOE_W2_DELTA_CAPTURE",
         "gate_fire_timing": "VLLM_MOE_W2_GATE_FIRE_TIMING",
         "gate_dump": "VLLM_MOE_W2_GATE_DUMP",
+        "bf12": "VLLM_MOE_W2_BF12",
+        "bf12_min_numel": "VLLM_MOE_W2_BF12_MIN_NUMEL",
+        "bf12_verify": "VLLM_MOE_W2_BF12_VERIFY",
+        "bf12_exclude": "VLLM_MOE_W2_BF12_EXCLUDE",
     }
 
     def __post_init__(self):

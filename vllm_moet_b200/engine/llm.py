@@ -151,6 +151,14 @@ class LLM:
             expert_source=self.expert_source)
         if self.expert_source is not None:
             self.expert_source.flush()
+        self.bf12_stats = None
+        if self.ecfg.moet.bf12:
+            # lossless 12-bit re-pack of the dense BF16 linears, before any capture (the GPU
+            # runner's dense linears are FP8, so there it finds nothing to convert)
+            from ..formats.bf12 import convert_model
+            m = self.ecfg.moet
+            self.bf12_stats = convert_model(self.mw, m.bf12_min_numel,
+                                            tuple(x for x in m.bf12_exclude.split(",") if x), m.bf12_verify)
         if speculative_method == "eagle3" and num_speculative_tokens > 0:
             from ..models.eagle3_model import attach_eagle3, random_eagle3_weights
             attach_eagle3(self.mw, random_eagle3_weights(self.mw, seed=seed))

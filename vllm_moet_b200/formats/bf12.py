@@ -113,3 +113,52 @@ class Bf12Linear:
 
     def dequant(self) -> torch.Tensor:
         return decode(self.b).float()
+
+    def to(self, device) -> "Bf12Linear":
+        out = object.__new__(Bf12Linear)
+        out.b, out.shape = self.b.to(device), self.shape
+        return out
+
+
+# Linear attributes of a decoder layer that may hold a dense BF16 matrix.
+_LAYER_LINEARS = ("qkv_a", "q_b", "kv_b", "o", "gate_up", "down", "shared_gate_up", "shared_down",
+                  "idx_wq", "idx_wk", "idx_ww")
+
+
+def convert_model(mw, min_numel: int = 1 << 20, exclude=(), verify: bool = True) -> dict:
+    """Re-pack every dense linear whose weight is exactly BF16 (a ``FloatLinear`` loaded from a
+    BF16 checkpoint) and has at least ``min_numel`` elements into a :class:`Bf12Linear`, after
+    load and before any graph capture.  Names containing an ``exclude`` substring stay as they
+    are (``layers.3.o``, ``mtp.layer.kv_b``, ...); with ``verify`` each container is decoded
+    and compared bit for bit with the live matrix, and a mismatch keeps the original.
+    FP8 / NVFP4 linears and the 2-bit experts are not BF16 and are never touched (the GPU
+    runner's dense layers are FP8, so there this converts nothing).  The reference's
+    behaviour: ``convert_model`` after load, opt-in (patch P:3997-4057).
+    -> {"converted", "skipped_verify", "bytes_before", "bytes_after"}."""
+    from ..models.weights import FloatLinear
+    stats = {"converted": 0, "skipped_verify": 0, "bytes_before": 0, "bytes_after": 0}
+    layers = [(f"layers.{i}", lw) for i, lw in enumerate(mw.layers)]
+    if getattr(mw, "mtp", None) is not None and getattr(mw.mtp, "layer", None) is not None:
+        layers.append(("mtp.layer", mw.mtp.layer))
+    for prefix, lw in layers:
+        for attr in _LAYER_LINEARS:
+            lin = getattr(lw, attr, None)
+            name = f"{prefix}.{attr}"
+            if not isinstance(lin, FloatLinear) or lin.w.dim() != 2 or lin.w.numel() < min_numel:
+                continue
+            if any(x in name for x in exclude):
+                continue
+            w = lin.w
+            wb = w.to(torch.bfloat16)
+            if not torch.equal(wb.float(), w.float()):
+                continue                    # not a BF16 matrix (e.g. fp32 random init)
+            new = Bf12Linear(wb)
+            if verify and not torch.equal(decode(new.b.to("cpu")).view(torch.int16), wb.cpu().view(torch.int16)):
+                stats["skipped_verify"] += 1
+                continue
+            stats["converted"] += 1
+            stats["bytes_before"] += wb.numel() * 2
+            b = new.b
+            stats["bytes_after"] += b.classes.numel() + b.lo.numel() + 16 + b.esc_pos.numel() * 9
+            setattr(lw, attr, new)
+    return stats
