@@ -39,7 +39,8 @@ def chain(prompt, n):
 
 class FakeRunner:
     def __init__(self, k):
-        self.k, self.graphs, self.steps = k, {}, 0
+        self.k, self.graphs, self.steps, self.nodraft_steps = k, {}, 0, 0
+        self.nodraft_graphs = {}
         self.ws_prefill = self
         self.logits = {}
         self.starts_log, self.copies, self.chunks = [], [], []
@@ -82,12 +83,25 @@ class FakeRunner:
         x[int(t)] = 10.0
         return x
 
-    def decode_body(self, st, sample=False):
+    def decode_body(self, st, sample=False, draft=True):
         self.steps += 1
         kp1 = self.k + 1
         lg = torch.zeros(st.B * kp1, V)
         if sample:
             return self._decode_sampled(st)
+        if not draft:                     # the no-draft step: one row per sequence, stale drafts kept
+            self.nodraft_steps += 1
+            for r in range(st.B):
+                if not int(st.active[r]):
+                    continue
+                toks, p = st.tokens[r].tolist(), int(st.seq_pos[r])
+                nxt = f(toks[0], p)
+                st.out_tokens[r] = torch.tensor([nxt] + [-1] * self.k, dtype=torch.int32)
+                st.n_acc[r] = 0
+                st.tokens[r] = torch.tensor([nxt] + toks[1:], dtype=torch.int32)
+                st.seq_pos[r] = p + 1
+            self.logits[st.B] = lg
+            return
         for r in range(st.B):
             if not int(st.active[r]):
                 continue
@@ -166,6 +180,8 @@ def engine(monkeypatch):
         llm.tokenizer = ByteTokenizer(V)
         llm._states, llm._DecodeState, llm._ids = {}, DecodeState, itertools.count()
         llm.cache = llm.delta = llm.gate = llm.routing = llm.timers = None
+        llm.spec_guard = llm.affinity = None
+        llm._spec_draft = True
         llm._tp_group = llm._pp_group = llm._ep_group = None
         llm._decode_steps, llm.stats = 0, {}
         llm._chunk_budget = chunk
@@ -285,6 +301,53 @@ def test_base_cache_misses_are_fetched_and_replayed(engine):
     assert [o.outputs[0].token_ids for o in out] == [chain([5, 6, 7], 9), chain([9, 9], 9)]
     assert llm.replay.stats["replayed_steps"] > 0 and cache.stats["fetched_rows"] > 0
     assert llm.kpi.snapshot()["replayed_steps"] == llm.replay.stats["replayed_steps"]
+
+
+def test_spec_guard_and_draft_affinity_on_the_cache_loop(engine):
+    """While the expert pool keeps replaying, the spec guard latches drafting off and the loop
+    runs the no-draft step (one row per sequence); greedy output is still the model's chain.
+    Draft-affinity learns token -> experts from each drafting step and prefetches the next
+    step's drafts' experts."""
+    from vllm_moet_b200.residency import ExpertCache, ReplayEngine, make_store
+    from vllm_moet_b200.residency.control import DraftAffinity, SpecGuard
+    from vllm_moet_b200.utils.observability import KpiLogger
+    llm = engine()
+    L, E, SB = 2, 64, 256          # 128 experts, 40 slots: a step's <= 36 fit, misses keep coming
+    st_ = make_store("pinned", L, E, SB)
+    for li in range(L):
+        st_.add_layer(li, torch.randint(0, 256, (E, SB), dtype=torch.uint8))
+    cache = ExpertCache(st_, L, E, SB, 40, device="cpu", manager=False)
+    llm.cache, llm.replay, llm.kpi = cache, ReplayEngine(cache, comm_device="cpu"), KpiLogger(every=10 ** 6)
+    llm.spec_guard = SpecGuard(alpha=0.6, hi=0.5, lo=0.05, patience=4)
+    llm.affinity = DraftAffinity(cache)
+    prefetched = []
+    real_prefetch = cache.request_prefetch
+    cache.request_prefetch = lambda pairs: (prefetched.append(list(pairs)), real_prefetch(pairs))[1]
+    route = {}
+    llm.runner.route_ids = lambda B: route.get(B, [None] * L)
+    real_step = llm.runner.decode_body
+
+    def step_with_routing(st, sample=False, draft=True):
+        toks = (st.tokens if draft else st.tokens[:, :1]).clone()
+        real_step(st, sample, draft)
+        ids = torch.tensor([[int(t) % E, (int(t) * 5 + 3) % E] for t in toks.reshape(-1).tolist()])
+        route[st.B] = [ids] * L
+        for li in range(L):
+            cache.miss_count += int((cache.slot_table[li, ids.reshape(-1)] < 0).sum())
+    llm.runner.decode_body = step_with_routing
+    prompts = [[5, 6, 7], [9, 9], [100, 3]]
+    out = llm.generate(prompts, SamplingParams(max_tokens=24, ignore_eos=True))
+    assert [o.outputs[0].token_ids for o in out] == [chain(p, 24) for p in prompts]
+    assert llm.runner.nodraft_steps > 0                       # the guard suppressed drafting
+    assert llm.runner.steps > llm.runner.nodraft_steps        # and let it resume
+    # the learned table drives prefetches of a learned token's non-resident experts
+    assert len(llm.affinity.table) > 0
+    toks = list(llm.affinity.table)[:8]
+    want = {(li, e) for t in toks for li, es in enumerate(llm.affinity.table[t]) for e in es
+            if not cache.resident(li, e)}
+    n = llm.affinity.prefetch(toks)
+    assert n == len(want) and (not want or set(prefetched[-1]) == want)
+    assert all(cache.resident(li, e) for li, e in want)
 
 
 def test_sampling_rows_share_the_batch_with_greedy_rows(engine):

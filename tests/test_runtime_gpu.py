@@ -74,6 +74,24 @@ def test_graph_equals_eager_and_is_deterministic(llm):
     assert a == c
 
 
+def test_nodraft_step_keeps_greedy_output(llm):
+    """The spec guard's no-draft step (main model over one row per sequence, no MTP pass;
+    its own captured graph) emits exactly the drafting engine's greedy tokens, and drafting
+    resumes on the stale drafts without changing them either."""
+    prompts = [_prompt(40, 61), _prompt(77, 62)]
+    sp = SamplingParams(max_tokens=12, ignore_eos=True)
+    want = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
+    llm._spec_draft = False
+    try:
+        got = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
+    finally:
+        llm._spec_draft = True
+    assert got == want
+    assert llm.runner.nodraft_graphs
+    again = [o.outputs[0].token_ids for o in llm.generate(prompts, sp)]
+    assert again == want
+
+
 def test_decode_tracks_reference_greedy(llm):
     """Teacher-forced check: every emitted token is the reference argmax given
     the emitted prefix, or a near-tie in the reference logits."""

@@ -235,6 +235,10 @@ class MoetConfig:
     delta_capture: Optional[str] = None  # .npy of per-step routed expert ids
     gate_fire_timing: bool = False      # promote / replay milliseconds per gate iteration
     gate_dump: Optional[str] = None     # JSONL: one row per gate evaluation
+    # spec guard (drafting latched off while the base pool replays) and draft-affinity prefetch
+    spec_guard: float = 60.0            # replay-EMA percent that suppresses drafting (0 = off)
+    spec_guard_ema: float = 0.02
+    prefetch: bool = False              # prefetch the experts the next step's drafts routed to before
     # bf12: lossless 12-bit container for dense BF16 linears, converted after load
     bf12: bool = False
     bf12_min_numel: int = 1 << 20
@@ -278,6 +282,9 @@ class MoetConfig:
         "delta_capture": "VLLM_MOE_W2_DELTA_CAPTURE",
         "gate_fire_timing": "VLLM_MOE_W2_GATE_FIRE_TIMING",
         "gate_dump": "VLLM_MOE_W2_GATE_DUMP",
+        "spec_guard": "VLLM_MOE_W2_SPEC_GUARD",
+        "spec_guard_ema": "VLLM_MOE_W2_SPEC_GUARD_EMA",
+        "prefetch": "VLLM_MOE_W2_PREFETCH",
         "bf12": "VLLM_MOE_W2_BF12",
         "bf12_min_numel": "VLLM_MOE_W2_BF12_MIN_NUMEL",
         "bf12_verify": "VLLM_MOE_W2_BF12_VERIFY",

@@ -111,6 +111,7 @@ class NativeRunner:
         self.scale = 1.0 / math.sqrt(cfg.qk_head_dim)
         self.graphs = {}
         self.sample_graphs = {}       # bucket -> graph of the speculative-sampling decode step
+        self.nodraft_graphs = {}      # bucket -> graph of the greedy step without drafts (spec guard)
         self.tp_group = None
         self.tp_rank, self.tp_size = mw.tp_rank, mw.tp_size
         self.ar = None            # fused peer-memory all-reduce (SymmAllReduce) for decode-sized steps
@@ -943,18 +944,51 @@ class NativeRunner:
             ws = self.ws_decode_by_bucket[B] = Workspace(self.dev)
         return ws
 
-    def decode_body(self, st, sample: bool = False):
+    def decode_body(self, st, sample: bool = False, draft: bool = True):
         """One MTP decode step over the device state `st` (all tensors static).
         Each batch bucket owns its workspace: a captured graph keeps the
         addresses it was recorded with.  `sample`: verify with speculative sampling
         (the state's per-row temperature / top-k / top-p / min-p / seed) instead of
-        greedy matching; rows at temperature 0 stay greedy."""
+        greedy matching; rows at temperature 0 stay greedy.  `draft=False`: the step
+        without drafts the spec guard switches to (greedy)."""
         prev = self.ws
         self.ws = self._bucket_ws(st.B)
         try:
-            self._decode_body(st, sample)
+            if draft or self.k == 0:
+                self._decode_body(st, sample)
+            else:
+                self._decode_body_nodraft(st)
         finally:
             self.ws = prev
+
+    def _decode_body_nodraft(self, st):
+        """A greedy decode step without drafts (the spec guard's choice while the expert pool
+        is cold): the main model over one row per sequence, no MTP pass, so the step routes
+        to the experts of one token per sequence instead of k + 1 plus the drafts'.  The
+        sequence advances by one token.  The state's stale drafts are verified -- and mostly
+        rejected -- by the next drafting step; the MTP layer's cache is not written for this
+        position, which can only lower the acceptance of later drafts, never the output."""
+        if self.pp_size > 1:
+            raise NotImplementedError("the no-draft decode step runs on one pipeline stage")
+        C = self.C
+        if self.cache is not None:
+            self.miss.zero_()
+        B = st.B
+        pos = st.seq_pos
+        blk = st.block_table.gather(1, (pos // KV_BLOCK).long().view(B, 1)).view(-1)
+        slot = blk.long() * KV_BLOCK + (pos % KV_BLOCK).long()
+        slot = torch.where(st.active.bool(), slot, torch.full_like(slot, -1))
+        ctx = StepCtx(T=B, pos=pos.int(), seq=st.arange_b, slot=slot, block_table=st.block_table, mode="decode",
+                      mb=8)
+        x = self._main(st.tokens[:, 0].contiguous(), ctx)
+        _, logits = self._final(x, None, "main")
+        am = self.ws.get("dec.am", (B,), torch.int32)
+        self._argmax(logits, am)
+        st.targets[:, 0].copy_(am)
+        st.n_acc.zero_()
+        st.out_tokens.fill_(-1)
+        st.out_tokens[:, 0].copy_(am)
+        C.mtp_finalize(st.targets, st.n_acc, st.drafts, st.tokens, st.seq_pos, st.active)
 
     def _sample_verify(self, st, logits):
         """Speculative sampling of the verify rows into targets / out_tokens / n_acc (the
@@ -1056,25 +1090,26 @@ class NativeRunner:
         C.mtp_finalize(st.targets, st.n_acc, st.drafts, st.tokens, st.seq_pos, st.active)
         self._pp_broadcast_state(st)
 
-    def capture(self, st, warm: bool = True, sample: bool = False):
+    def capture(self, st, warm: bool = True, sample: bool = False, draft: bool = True):
         """Capture decode_body for the state's batch bucket (after one eager warm-up);
-        the sampling variant is a second graph of the bucket (`sample_graphs`)."""
+        the sampling variant is a second graph of the bucket (`sample_graphs`), the
+        no-draft step a third (`nodraft_graphs`)."""
         if warm:
-            self.decode_body_eager_warm(st, sample)
+            self.decode_body_eager_warm(st, sample, draft)
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
             with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
-                self.decode_body(st, sample)
+                self.decode_body(st, sample, draft)
         torch.cuda.current_stream().wait_stream(s)
-        (self.sample_graphs if sample else self.graphs)[st.B] = g
+        (self.sample_graphs if sample else self.graphs if draft else self.nodraft_graphs)[st.B] = g
         self._bucket_ws(st.B).frozen = True
         return g
 
-    def decode_body_eager_warm(self, st, sample: bool = False):
+    def decode_body_eager_warm(self, st, sample: bool = False, draft: bool = True):
         snap = st.snapshot()
-        self.decode_body(st, sample)
+        self.decode_body(st, sample, draft)
         st.restore(snap)
         torch.cuda.synchronize()
 

@@ -196,6 +196,8 @@ class LLM:
                 self.runner.set_pp_group(pp_group)
                 self.ecfg.cuda_graphs = False      # pipeline stages run eager steps (p2p per step)
             self.cache = self.replay = None
+            self.spec_guard = self.affinity = None
+            self._spec_draft = True
             slots = expert_cache_slots
             if not slots and self.ecfg.moet.base_cache_gb > 0:
                 from ..residency import moe_layers
@@ -334,7 +336,9 @@ class LLM:
 
     def _attach_cache(self, slots, kind, store_dir, tp_group):
         """Routed experts from a host store through a GPU expert cache of `slots` slots,
-        with in-graph miss counting and fixed-point replay of missed decode steps."""
+        with in-graph miss counting and fixed-point replay of missed decode steps; the spec
+        guard (VLLM_MOE_W2_SPEC_GUARD, replay-EMA percent) and draft-affinity prefetch
+        (VLLM_MOE_W2_PREFETCH=1) ride on the same loop."""
         from ..residency import ReplayEngine, build_expert_cache, checkpoint_id, rank_suffix
         m = self.ecfg.moet
         kw = {}
@@ -346,6 +350,9 @@ class LLM:
                 raise ValueError("pack / tiered expert stores need a store directory (VLLM_MOE_W2_STORE_DIR)")
         from ..utils.observability import KpiLogger
         self.kpi = KpiLogger(every=m.kpi_every)
+        from ..residency.control import DraftAffinity, SpecGuard
+        self.spec_guard = (SpecGuard(alpha=m.spec_guard_ema, hi=m.spec_guard / 100.0, lo=m.spec_guard / 200.0)
+                           if m.spec_guard > 0 and self.k > 0 and self._pp_group is None else None)
         from ..residency import moe_layers, working_set_floor
         floor = working_set_floor(len(moe_layers(self.mw)), self.cfg.top_k, self.k, self.ecfg.max_num_seqs,
                                   self.cfg.num_experts)
@@ -357,6 +364,7 @@ class LLM:
         self.replay = ReplayEngine(self.cache, tp_group=tp_group, pp_group=self._pp_group, mode=m.replay_mode,
                                    fp_max=m.fp_max,
                                    miss_tol=m.base_miss_tol)
+        self.affinity = DraftAffinity(self.cache) if m.prefetch and self.k > 0 else None
 
     # ------------------------------------------------------------------ API
     def _normalize(self, prompts) -> List[List[int]]:
@@ -741,11 +749,15 @@ class LLM:
             # a batch with a sampling row runs the bucket's speculative-sampling variant
             sample = any(r is not None and (r.params.temperature > 0 or r.params.processes_logits) for r in rows)
             self._step_sample = sample
+            # spec guard: greedy batches switch to the no-draft step while the pool replays
+            draft = self._spec_draft or sample or self.delta is not None
+            self._step_draft = draft
             graph = None
             if self.ecfg.cuda_graphs:
-                graph = (runner.sample_graphs if sample else runner.graphs).get(B)
+                graph = (runner.sample_graphs if sample else runner.graphs if draft else runner.nodraft_graphs).get(B)
                 if graph is None:
-                    graph = runner.capture(st, **({"sample": True} if sample else {}))
+                    graph = runner.capture(st, **({"sample": True} if sample else {}),
+                                           **({} if draft else {"draft": False}))
             t0 = time.perf_counter()
             if self.delta is not None:
                 self._delta_snap = st.snapshot()
@@ -759,6 +771,14 @@ class LLM:
                 self.cache.step_end()
                 self.kpi.step(replayed=n_rep > 0, misses=self.cache.stats["fetched_rows"] - f0,
                               fetched_rows=self.cache.stats["fetched_rows"] - f0)
+                if self.spec_guard is not None:
+                    self._spec_draft = self.spec_guard.observe(n_rep > 0)
+                if self.affinity is not None and draft:
+                    # learn token -> experts from this step's verify rows, then prefetch what the
+                    # next step's drafts routed to before (asynchronously, off the decode stream)
+                    self.affinity.record(snap[0].reshape(-1).tolist(),
+                                         [t if t is not None and t.dim() == 2 else None for t in runner.route_ids(B)])
+                    self.affinity.prefetch(st.tokens[:, 1:].reshape(-1).tolist())
             elif graph is not None:
                 graph.replay()
             else:
@@ -952,6 +972,8 @@ class LLM:
     def _decode_eager(self, st):
         if getattr(self, "_step_sample", False):
             self.runner.decode_body(st, True)
+        elif not getattr(self, "_step_draft", True):
+            self.runner.decode_body(st, draft=False)
         else:
             self.runner.decode_body(st)
 
