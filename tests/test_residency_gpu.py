@@ -156,3 +156,39 @@ def test_traces_and_dumps(tmp_path, monkeypatch):
     assert len(rows) == llm._decode_steps and any(r["fired"] > 0 for r in rows)
     fired = [it for r in rows for it in r["iters"]]
     assert fired and all(it["promote_ms"] >= 0 and it["replay_ms"] > 0 for it in fired)
+
+
+@pytest.mark.parametrize("pf4", ["1", "0"])
+def test_prefill_fp4(pf4, monkeypatch):
+    """Prefill-FP4 (VLLM_MOE_W2_PREFILL_FP4, default on): with every expert holding a direct-8
+    delta slot, the prefill's last logits track the fp32 oracle over the FP4 (MXFP4) experts
+    and not the one over the 2-bit base; with it off, the other way round."""
+    from vllm_moet_b200.models import reference
+    from vllm_moet_b200.residency import moe_layers
+    from vllm_moet_b200.residency.delta import dequant_delta_slot
+    monkeypatch.setenv("VLLM_MOE_W2_PREFILL_FP4", pf4)
+    llm = LLM(_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=512, max_num_seqs=2,
+              delta_slots=48, gate=True)
+    llm.gate.tau = -1.0
+    layers = moe_layers(llm.mw)
+    llm.delta.promote([(li, e) for li in range(len(layers)) for e in range(16)])
+    p = _prompts()[1]
+    llm.generate([p], SamplingParams(max_tokens=1, ignore_eos=True))
+    lg = llm.runner.ws_prefill.bufs[("main.logits", torch.float32)][: llm.cfg.vocab].clone()
+    cs = reference.rope_cos_sin(llm.cfg, 256, "cuda")
+    t = torch.tensor(p, device="cuda")
+    base = reference.forward(llm.mw, t, torch.arange(len(p), device="cuda"), cs)[0][-1]
+    lay = layers[0].experts.layout
+    for li, lw in enumerate(layers):
+        rows = llm.delta.store.layers[li]
+        d = [dequant_delta_slot(rows[e].cpu(), lay.H, lay.I) for e in range(rows.shape[0])]
+        lw.experts.dense_w13 = torch.stack([a for a, _ in d]).cuda()
+        lw.experts.dense_w2 = torch.stack([b for _, b in d]).cuda()
+    fp4 = reference.forward(llm.mw, t, torch.arange(len(p), device="cuda"), cs)[0][-1]
+    rel = lambda a, b: float((a - b).norm() / b.norm())     # noqa: E731
+    e_fp4, e_base = rel(lg, fp4), rel(lg, base)
+    if pf4 == "1":
+        assert e_fp4 < e_base, (e_fp4, e_base)
+    else:
+        assert e_base < e_fp4, (e_fp4, e_base)
+    llm.shutdown()

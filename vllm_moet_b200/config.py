@@ -205,6 +205,7 @@ class MoetConfig:
     delta_policy: str = "freq"          # freq | need | lru
     delta_split: bool = False
     delta_tick_ms: float = 50.0
+    prefill_fp4: str = "1"              # "1": prefill serves delta-slot experts at FP4 too; "0": base only
     delta_decay: float = 0.98
     # base cache (GPU as expert cache)
     base_cache_gb: float = 0.0
@@ -256,6 +257,7 @@ class MoetConfig:
         "delta_policy": "VLLM_MOE_W2_DELTA_POLICY",
         "delta_split": "VLLM_MOE_W2_DELTA_SPLIT",
         "delta_tick_ms": "VLLM_MOE_W2_DELTA_TICK_MS",
+        "prefill_fp4": "VLLM_MOE_W2_PREFILL_FP4",
         "delta_decay": "VLLM_MOE_W2_DELTA_DECAY",
         "base_cache_gb": "VLLM_MOE_W2_BASE_CACHE_GB",
         "base_miss_tol": "VLLM_MOE_W2_BASE_MISS_TOL",

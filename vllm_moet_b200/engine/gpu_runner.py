@@ -580,6 +580,10 @@ class NativeRunner:
         E_loc = ex.n_local if ep else E
         e_lo = ex.e_lo if ep else -1
         use_tc = ctx.mode in ("prefill", "cached") and H % 128 == 0 and I % 128 == 0 and (2 * I) % 128 == 0
+        if use_tc and self.delta is not None and self.ecfg.moet.prefill_fp4 not in ("0", ""):
+            # prefill-FP4: experts holding a delta slot are served at FP4 in prefill as in decode;
+            # the tcgen05 prefill GEMM reads only the 2-bit base, so the delta-aware GEMV runs
+            use_tc = False
         topp = self.ecfg.moet.topp
         if self.ep is not None:
             # DP attention + EP: route over all experts, then the all-to-all around the owners' kernels
