@@ -551,7 +551,9 @@ void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out) {
               w.is_contiguous() && H % 256 == 0, "router_logits: bf16 contiguous, H % 256 == 0");
   if (T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  if (T > 64 && E % 64 == 0 && H % 64 == 0 && out.is_contiguous()) {   // prefill-sized: tensor-core tiles
+  // prefill-sized T: tensor-core tiles (a 64 x 64 tile per CTA walks all of K, so decode-sized
+  // T -- a handful of CTAs -- stays on the warp-per-expert kernel, which spreads E over the GPU)
+  if (T >= 256 && E % 64 == 0 && H % 64 == 0 && out.is_contiguous()) {
     launch_k(router_logits_mma_kernel, dim3((T + 63) / 64, E / 64), 128, 0, stream, (const __nv_bfloat16*)x.data_ptr(),
              T, H, (const __nv_bfloat16*)w.data_ptr(), E, out.data_ptr<float>());
     C10_CUDA_KERNEL_LAUNCH_CHECK();
