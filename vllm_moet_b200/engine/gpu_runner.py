@@ -117,6 +117,8 @@ class NativeRunner:
         self.ar = None            # fused peer-memory all-reduce (SymmAllReduce) for decode-sized steps
         self.ep = None            # expert-parallel all-to-all buffers (EpSymm) under DP attention + EP
         self.ep_group = None
+        self.sp_group = None      # sequence-parallel prefill ranks (replicated weights)
+        self._sp = None           # active SP prefill: (group, world, rank, block ids per rank's chunk)
         self.cache = None         # residency.ExpertCache when routed experts are served from a host store
         self.delta = None         # residency.DeltaTier (FP4 hot experts) when enabled
         self._moe_index = {}
@@ -313,6 +315,71 @@ class NativeRunner:
         res[order] = back
         return res
 
+    def set_sp_group(self, group):
+        """Sequence-parallel prefill over `group` (every rank holds the whole model): a long
+        prompt is split into block-aligned chunks, rank r runs chunk r through every layer,
+        and before each layer's attention (and the DSA indexer's scores) the ranks all-gather
+        their chunks' blocks of that layer's paged caches, so chunk r attends to every earlier
+        position.  Afterwards every rank holds the prompt's full caches and decodes it
+        (replicated, deterministic)."""
+        self.sp_group = group
+
+    def sp_chunk(self, n: int):
+        """-> (chunk length, block-aligned) of an n-token prompt over the SP group, or None
+        when some rank would get no token (a short prompt prefills replicated)."""
+        import torch.distributed as dist
+        W = dist.get_world_size(self.sp_group)
+        Tc = -(-(-(-n // W)) // KV_BLOCK) * KV_BLOCK
+        return Tc if (W - 1) * Tc < n else None
+
+    def prefill_sp(self, prompt: list, block_table: list, row: int, state):
+        """Sequence-parallel prefill of one prompt into decode-state row `row` -> first token
+        (the same on every rank).  Rank r computes positions [r * Tc, min(n, (r + 1) * Tc)):
+        a non-final chunk as `prefill_chunk`, the rank holding the last position as the final
+        chunk (head, first token, MTP drafts); that rank then broadcasts the row's state."""
+        import torch.distributed as dist
+        G = self.sp_group
+        W, r = dist.get_world_size(G), dist.get_rank(G)
+        n = len(prompt)
+        Tc = self.sp_chunk(n)
+        assert Tc is not None, "sp prefill: prompt too short for the group"
+        nb = Tc // KV_BLOCK
+        bt = torch.tensor(block_table, dtype=torch.long)
+        blocks = torch.stack([bt[q * nb:(q + 1) * nb] for q in range(W)]).to(self.dev)
+        self._sp = (G, W, r, blocks)
+        lo, hi = r * Tc, min(n, (r + 1) * Tc)
+        owner = (n - 1) // Tc
+        try:
+            if r == owner:
+                first = self.prefill([prompt], [block_table], [row], state, starts=[lo] if lo else None)
+            else:
+                self.prefill_chunk(prompt, block_table, lo, hi)
+        finally:
+            self._sp = None
+        src = dist.get_global_rank(G, owner)
+        rows = torch.tensor([row], device=self.dev)
+        tok, pos = state.tokens[rows].contiguous(), state.seq_pos[rows].contiguous()
+        dist.broadcast(tok, src=src, group=G)
+        dist.broadcast(pos, src=src, group=G)
+        state.tokens[rows] = tok
+        state.seq_pos[rows] = pos
+        return int(tok[0, 0])
+
+    def _sp_gather(self, caches, li):
+        """All-gather of layer li's cache blocks of every rank's SP chunk (a no-op outside an
+        SP prefill).  Block ids are the same on every rank (one block table)."""
+        if self._sp is None or li >= len(caches) or caches[li] is None:
+            return
+        import torch.distributed as dist
+        G, W, r, blocks = self._sp
+        cache = caches[li]
+        mine = cache.index_select(0, blocks[r]).contiguous()
+        out = torch.empty((W,) + tuple(mine.shape), dtype=mine.dtype, device=mine.device)
+        dist.all_gather_into_tensor(out, mine, group=G)
+        for q in range(W):
+            if q != r:
+                cache.index_copy_(0, blocks[q], out[q])
+
     def attach_expert_cache(self, cache):
         """Serve routed experts through `cache` (pools already rewired by
         residency.build_expert_cache).  Kernels count misses into cache.miss_count;
@@ -495,6 +562,7 @@ class NativeRunner:
             C.gemv_fp8(qnq.permute(1, 0, 2), qns.permute(1, 0, 2), lw.w_uk_t.w, lw.w_uk_t.s,
                        qcat[:, :, :lat].permute(1, 0, 2), None)
             self._join()
+            self._sp_gather(self.kv, li)      # SP prefill: the other ranks' chunks of this layer's cache
             S = max(1, min(32, 256 // T))
             opart = self.ws.get("opart", (S, T, Hh, lat), torch.float32)
             mlp = self.ws.get("mlpart", (S, T, Hh, 2), torch.float32)
@@ -506,6 +574,7 @@ class NativeRunner:
             kr = self.ws.get("kr", (T, rope), torch.bfloat16)
             C.kv_prep(qkva[:, ql:], lat, rope, lw.kv_a_norm, cfg.rms_eps, ctx.pos, self.cos_sin, ctx.slot,
                       self.kv_mode, cache, None, kr, latq, lats, self.status)
+            self._sp_gather(self.kv, li)      # SP prefill, first chunk: its rows to the other ranks
             kvb = self.ws.get("kvb", (T, Hh * (nope + vd)), torch.bfloat16)
             self._gemv(latq, lats, lw.kv_b, kvb)
             qf = self.ws.get("qfull", (T, Hh, nope + rope), torch.bfloat16)
@@ -524,6 +593,7 @@ class NativeRunner:
         ki = self.ws.get("idx.k", (T, Di), torch.bfloat16)
         self._gemv(hq, hs, lw.idx_wk, ki)
         C.idx_k_write(ki, ctx.slot, self.idx_kv[li], self.status)
+        self._sp_gather(self.idx_kv, li)      # SP prefill: the other ranks' indexer keys
         if ctx.mode == "prefill":
             return None
         qi = self.ws.get("idx.q", (T, Hi * Di), torch.bfloat16)

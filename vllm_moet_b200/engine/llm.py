@@ -76,8 +76,11 @@ class LLM:
             device = "cuda" if torch.cuda.is_available() else "cpu"
         self.device = torch.device(device)
         self._tp_group, self._pp_group = tp_group, pp_group
-        if self.device.type == "cuda" and (sp_group is not None or dcp_group is not None):
-            raise NotImplementedError("SP prefill / DCP decode run on the CPU engine")
+        if self.device.type == "cuda" and dcp_group is not None:
+            raise NotImplementedError("DCP decode runs on the CPU engine")
+        if self.device.type == "cuda" and sp_group is not None and (enable_prefix_caching or enable_chunked_prefill):
+            raise NotImplementedError("GPU SP prefill: no prefix caching or chunked prefill")
+        self._sp_group = sp_group
         self._ep_group = ep_group
         if speculative_method not in ("mtp", "dspark", "dflash", "eagle3"):
             raise ValueError(f"speculative_method {speculative_method!r}: mtp | dspark | dflash | eagle3")
@@ -186,6 +189,8 @@ class LLM:
                                               "chunked prefill")
                 ep_partition(self.mw, dist.get_rank(ep_group), dist.get_world_size(ep_group))
             self.runner = NativeRunner(self.mw, self.ecfg, nb, self.device)
+            if sp_group is not None:
+                self.runner.set_sp_group(sp_group)
             if ep_group is not None:
                 # the most routed rows of one decode-sized layer on one rank: verify rows x top-k
                 self.runner.set_ep_group(ep_group, self._bucket(max_num_seqs) * (self.k + 1) * cfg.top_k)
@@ -913,7 +918,12 @@ class LLM:
         bts = [bt_host[r.row].tolist() for r in adm]
         with self.timers.span("prefill") if self.timers is not None else contextlib.nullcontext():
             kw = dict(({"sample": True} if sample_pf else {}), **({"starts": starts} if any(starts) else {}))
-            firsts = runner.prefill([r.prompt for r in adm], bts, [r.row for r in adm], st, **kw).tolist()
+            sp = getattr(self, "_sp_group", None) is not None and not sample_pf and not any(starts)
+            if sp and all(runner.sp_chunk(len(r.prompt)) is not None for r in adm):
+                # sequence-parallel prefill, one prompt at a time over the group's ranks
+                firsts = [runner.prefill_sp(r.prompt, bt, r.row, st) for r, bt in zip(adm, bts)]
+            else:
+                firsts = runner.prefill([r.prompt for r in adm], bts, [r.row for r in adm], st, **kw).tolist()
         if getattr(self.blocks, "prefix_caching", False):
             for r in adm:
                 self.blocks.register(r.rid, r.prompt)
