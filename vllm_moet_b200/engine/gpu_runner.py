@@ -367,7 +367,8 @@ class NativeRunner:
 
     def _sp_gather(self, caches, li):
         """All-gather of layer li's cache blocks of every rank's SP chunk (a no-op outside an
-        SP prefill).  Block ids are the same on every rank (one block table)."""
+        SP prefill; callers skip decode-mode passes, e.g. the owner's MTP draft chain).  Block
+        ids are the same on every rank (one block table)."""
         if self._sp is None or li >= len(caches) or caches[li] is None:
             return
         import torch.distributed as dist
@@ -562,7 +563,8 @@ class NativeRunner:
             C.gemv_fp8(qnq.permute(1, 0, 2), qns.permute(1, 0, 2), lw.w_uk_t.w, lw.w_uk_t.s,
                        qcat[:, :, :lat].permute(1, 0, 2), None)
             self._join()
-            self._sp_gather(self.kv, li)      # SP prefill: the other ranks' chunks of this layer's cache
+            if ctx.mode != "decode":
+                self._sp_gather(self.kv, li)  # SP prefill: the other ranks' chunks of this layer's cache
             S = max(1, min(32, 256 // T))
             opart = self.ws.get("opart", (S, T, Hh, lat), torch.float32)
             mlp = self.ws.get("mlpart", (S, T, Hh, 2), torch.float32)
@@ -593,7 +595,8 @@ class NativeRunner:
         ki = self.ws.get("idx.k", (T, Di), torch.bfloat16)
         self._gemv(hq, hs, lw.idx_wk, ki)
         C.idx_k_write(ki, ctx.slot, self.idx_kv[li], self.status)
-        self._sp_gather(self.idx_kv, li)      # SP prefill: the other ranks' indexer keys
+        if ctx.mode != "decode":
+            self._sp_gather(self.idx_kv, li)  # SP prefill: the other ranks' indexer keys
         if ctx.mode == "prefill":
             return None
         qi = self.ws.get("idx.q", (T, Hi * Di), torch.bfloat16)
