@@ -49,6 +49,9 @@ def main():
                     help="data-parallel attention + expert-parallel MoE (BASELINE config 3): every rank serves its "
                          "own streams, routed experts are partitioned over the ranks and exchanged all-to-all")
     ap.add_argument("--ep-streams", default="1,4,8,16,32", help="--ep: total concurrent streams to measure")
+    ap.add_argument("--sp", type=int, default=0,
+                    help="sequence-parallel prefill of one prompt of this many tokens over the N ranks "
+                         "(replicated weights); reports prefill tok/s, device-timed, max over ranks")
     ap.add_argument("--expert-cache-gb", type=float, default=0.0,
                     help="residency: serve routed experts from a GPU cache of this many GiB over a host store "
                          "(reports 1-stream decode through LLM.generate, host fetches included)")
@@ -86,6 +89,8 @@ def main():
                   max_num_seqs=max(per_rank, 1), num_layers=args.layers, seed=0, ep_group=dist.group.WORLD)
     elif args.expert_cache_gb > 0 or args.delta_slots > 0:
         return _residency(args, world, rank, local)
+    elif args.sp:
+        return _sp_prefill(args, world, rank, local, dist)
     else:
         llm = LLM("ds4-flash-shape", device="cuda", num_speculative_tokens=2, max_model_len=max_len,
                   max_num_seqs=args.streams, num_layers=args.layers, seed=0, tensor_parallel_size=world,
@@ -275,6 +280,57 @@ def main():
         dist.barrier()
         sys.stdout.flush()
         sys.stderr.flush()
+        os._exit(0)
+    return 0
+
+
+def _sp_prefill(args, world, rank, local, dist):
+    """Sequence-parallel prefill on the DS4 shape: one prompt of --sp tokens split into
+    block-aligned chunks over the ranks (each holds the whole model), per-layer all-gathers
+    of the cache blocks before attention.  Device-timed (CUDA events, barrier + synchronize
+    on both sides), max over ranks; one GPU runs the plain prefill of the same prompt."""
+    import torch
+    from vllm_moet_b200 import LLM
+    n = args.sp
+    llm = LLM("ds4-flash-shape", device="cuda", num_speculative_tokens=2, max_model_len=n + 256, max_num_seqs=1,
+              num_layers=args.layers, seed=0, sp_group=dist.group.WORLD if world > 1 else None)
+    g = torch.Generator().manual_seed(99)
+    prompt = torch.randint(3, llm.cfg.vocab, (n,), generator=g).tolist()
+    st = llm._state(1)
+    blocks = llm.blocks.allocate("sp", n + 64)
+    bt = [0] * llm.max_blocks
+    bt[:len(blocks)] = blocks
+    st.block_table[0, :len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
+    run = (lambda: llm.runner.prefill_sp(prompt, bt, 0, st)) if world > 1 else \
+        (lambda: llm.runner.prefill([prompt], [bt], [0], st))
+    for _ in range(max(1, args.warmup - 2)):
+        run()
+    times = []
+    for _ in range(3):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        first = run()
+        e.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([s.elapsed_time(e)], device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        times.append(float(t))
+    ms = min(times)
+    if rank == 0:
+        print(json.dumps({"metric": "prefill tok/s, one prompt, DS4-Flash shape [SP prefill]",
+                          "value": round(n * 1000.0 / ms, 1), "unit": "tok/s", "n_gpus": world, "prompt_tokens": n,
+                          "ms": round(ms, 2), "higher_is_better": True, "scaling": "strong",
+                          "parallelism": f"sp{world} (replicated weights, per-layer cache all-gather)" if world > 1
+                          else "single", "first_token": int(first) if not hasattr(first, "tolist") else
+                          int(first.tolist()[0]), "dtype": "bf16 activations; fp8 dense; 2-bit experts",
+                          "data": "synthetic prompt, random-init weights"}), flush=True)
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
         os._exit(0)
     return 0
 
