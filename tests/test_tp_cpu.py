@@ -105,3 +105,27 @@ def test_tp2_unseeded_sampling_agrees_across_ranks():
     every rank, so both ranks emit the same tokens."""
     a, b = run_ranks(_tp_unseeded_sampling, 2)
     assert a == b
+
+
+def _tp_forward_replicated_attention(rank, world):
+    import torch.distributed as dist
+    cfg = tiny_config()
+    toks = torch.tensor([5, 17, 300, 42, 7, 99, 3, 250])
+    pos = torch.arange(len(toks))
+    cs = ref.rope_cos_sin(cfg, 64)
+    want, _ = ref.forward(random_weights(cfg, "cpu", seed=6), toks, pos, cs)
+    mw = random_weights(cfg, "cpu", seed=6, tp_rank=rank, tp_size=world, attn_tp=False)
+    lw = mw.layers[0]
+    with ref.tp_context(dist.group.WORLD):
+        got, _ = ref.forward(mw, toks, pos, cs)
+    return float((got - want).abs().max()), float(want.abs().max()), lw.attn_tp, tuple(lw.o.shape)
+
+
+def test_tp2_replicated_attention_matches_single_rank():
+    """Replicated TP attention (whole attention on every rank, experts / FFN sharded): the
+    attention output is not reduced, the FFN partials are, and the logits equal one rank."""
+    res = run_ranks(_tp_forward_replicated_attention, 2)
+    cfg = tiny_config()
+    for err, scale, attn_tp, o_shape in res:
+        assert not attn_tp and o_shape == (cfg.hidden, cfg.num_heads * cfg.v_head_dim)
+        assert err <= 1e-4 * max(scale, 1.0), (err, scale)

@@ -95,12 +95,13 @@ def _small_cfg():
                             dense_intermediate=512, num_heads=8, q_lora_rank=256, top_k=4)
 
 
-def _tp_engine(rank, world, fused, ep=False):
+def _tp_engine(rank, world, fused, ep=False, attn="shard"):
     import torch.distributed as dist
     from vllm_moet_b200 import SamplingParams
     from vllm_moet_b200.engine.llm import LLM
     from vllm_moet_b200.models import reference
     os.environ["MOET_TP_FUSED"] = "1" if fused else "0"     # read by set_tp_group
+    os.environ["MOET_TP_ATTN"] = attn                         # read by LLM (random-init weights)
     cfg = _small_cfg()
     llm = LLM(cfg, device="cuda", num_speculative_tokens=2, max_model_len=512, max_num_seqs=2,
               tensor_parallel_size=world, tp_group=dist.group.WORLD, tp_rank=rank, expert_parallel=ep)
@@ -158,6 +159,17 @@ def test_pp2_matches_single_gpu():
 def test_ep2_engine_tracks_oracle():
     """Expert parallelism inside the TP group (each rank owns half of the experts whole)."""
     res = run_ranks(_tp_engine, 2, False, True, backend="nccl", env={"NCCL_NVLS_ENABLE": "0"})
+    (o0, w0), (o1, w1) = res
+    assert o0 == o1 and all(len(o) == 10 for o in o0)
+    assert max(w0, w1) < 0.5, (w0, w1)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_replicated_attention_engine_tracks_oracle():
+    """TP2 with replicated attention (whole attention per rank, no o_proj reduction; experts
+    and dense FFN sharded and reduced): identical tokens on both ranks, each the oracle's argmax
+    or a near-tie under the same replication."""
+    res = run_ranks(_tp_engine, 2, False, False, "replicate", backend="nccl", env={"NCCL_NVLS_ENABLE": "0"})
     (o0, w0), (o1, w1) = res
     assert o0 == o1 and all(len(o) == 10 for o in o0)
     assert max(w0, w1) < 0.5, (w0, w1)

@@ -87,7 +87,9 @@ class NativeRunner:
         self.dev = torch.device(device)
         has_mtp = mw.mtp is not None or (mw.extra.get("pp_size", 1) > 1 and mw.cfg.num_mtp_layers > 0)
         self.k = ecfg.num_speculative_tokens if has_mtp else 0
-        self.Hh = self.cfg.num_heads // mw.tp_size
+        # heads per rank: all of them when attention is replicated across the TP group
+        attn_tp = all(getattr(lw, "attn_tp", True) for lw in mw.layers)
+        self.Hh = self.cfg.num_heads // mw.tp_size if attn_tp else self.cfg.num_heads
         cfg = self.cfg
         self.num_blocks = num_blocks
         self.kv_mode = 2 if ecfg.kv_cache_dtype == "nvfp4" else 1
@@ -583,7 +585,10 @@ class NativeRunner:
             C.q_prep(qb, Hh, nope, rope, ctx.pos, self.cos_sin, None, None, None, 0, qf)
             C.mla_prefill(qf, kvb.view(T, Hh, nope + vd), kr, ctx.cu_seqlens, ctx.max_len, self.scale,
                           ovq, ovs, None)
-        self._row_parallel_out(ovq, ovs, lw.o, x, out, T)
+        if getattr(lw, "attn_tp", True):
+            self._row_parallel_out(ovq, ovs, lw.o, x, out, T)
+        else:       # replicated attention: the whole o projection, residual added, no reduction
+            self._gemv(ovq, ovs, lw.o, out, x)
 
     def _indexer(self, lw, hq, hs, qaq, qas, ctx, li):
         """DSA indexer: insert this step's keys, score every cached position

@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import contextlib
 import itertools
+import os
 import time
 from collections import deque
 from dataclasses import dataclass, field
@@ -56,7 +57,8 @@ class LLM:
                  dcp_group=None, dcp_interleave: int = 1, ep_group=None, speculative_method: str = "mtp",
                  dspark: Optional[dict] = None, enable_prefix_caching: bool = False,
                  prefix_block_size: int = 16, enable_chunked_prefill: bool = False,
-                 max_num_batched_tokens: Optional[int] = None, **model_overrides):
+                 max_num_batched_tokens: Optional[int] = None, tp_attention: Optional[str] = None,
+                 **model_overrides):
         from ..models.loader import hf_config, is_checkpoint_dir, load_weights
         ckpt = model if is_checkpoint_dir(model) else None
         if ckpt is not None:
@@ -146,12 +148,21 @@ class LLM:
                                    with_mtp=num_speculative_tokens > 0, pp_rank=pp_rank,
                                    pp_size=pipeline_parallel_size, expert_parallel=expert_parallel,
                                    expert_source=self.expert_source)
+        # TP attention: "shard" (heads split, o_proj reduced) or "replicate" (whole attention on
+        # every rank, no o_proj reduction: half the decode reductions for ~42 MB / layer of FP8
+        # weights read per rank); MOET_TP_ATTN picks the default
+        tp_attention = tp_attention or os.environ.get("MOET_TP_ATTN", "shard")
+        if tp_attention not in ("shard", "replicate"):
+            raise ValueError("tp_attention: shard | replicate")
+        if tp_attention == "replicate" and tensor_parallel_size > 1 and (ckpt is not None or weights is not None
+                                                                         or expert_parallel):
+            raise NotImplementedError("replicated TP attention: random-init weights with sharded experts")
         self.mw = weights if weights is not None else random_weights(
             cfg, self.device, seed=seed, tp_rank=tp_rank, tp_size=tensor_parallel_size,
             with_mtp=num_speculative_tokens > 0, pp_rank=pp_rank, pp_size=pipeline_parallel_size,
             with_delta=(("split" if self.ecfg.moet.delta_split else True) if delta_slots and self.device.type == "cuda"
                         else False), expert_parallel=expert_parallel,
-            expert_source=self.expert_source)
+            expert_source=self.expert_source, attn_tp=tp_attention == "shard")
         if self.expert_source is not None:
             self.expert_source.flush()
         self.bf12_stats = None

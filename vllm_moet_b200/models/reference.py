@@ -328,15 +328,16 @@ def decoder_layer(cfg, lw, x, positions, cs, cache=None, li=0):
     """x [T, H], or [T, n, H] residual streams when the layer has hyper-connections."""
     if lw.hc_attn is not None:
         h, post, comb = hc_pre(cfg, lw.hc_attn, x)
-        a = _allreduce((_ATTN_IMPL or attention)(cfg, lw, rms_norm(h, lw.attn_norm, cfg.rms_eps), positions, cs,
-                                                 cache, li))
+        a = (_ATTN_IMPL or attention)(cfg, lw, rms_norm(h, lw.attn_norm, cfg.rms_eps), positions, cs, cache, li)
+        a = _allreduce(a) if lw.attn_tp else a        # replicated attention: the whole output on every rank
         x = hc_post(a, x, post, comb)
         h, post, comb = hc_pre(cfg, lw.hc_ffn, x)
         h = rms_norm(h, lw.ffn_norm, cfg.rms_eps)
         f = _allreduce((_MOE_IMPL or moe_block)(cfg, lw, h) if lw.is_moe else dense_ffn(cfg, lw, h))
         return hc_post(f, x, post, comb)
     h = rms_norm(x, lw.attn_norm, cfg.rms_eps)
-    x = x + _allreduce((_ATTN_IMPL or attention)(cfg, lw, h, positions, cs, cache, li))
+    a = (_ATTN_IMPL or attention)(cfg, lw, h, positions, cs, cache, li)
+    x = x + (_allreduce(a) if lw.attn_tp else a)    # replicated attention: the whole output on every rank
     h = rms_norm(x, lw.ffn_norm, cfg.rms_eps)
     return x + _allreduce((_MOE_IMPL or moe_block)(cfg, lw, h) if lw.is_moe else dense_ffn(cfg, lw, h))
 

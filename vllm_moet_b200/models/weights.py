@@ -198,6 +198,7 @@ class LayerWeights:
     idx_wk: object = None          # [D, H] indexer key (from the normed hidden)
     idx_ww: object = None          # [Hi, H] per-head weights (softmax-free, scaled by 1/sqrt(Hi*D))
     # hyper-connections (cfg.hc_mult > 1)
+    attn_tp: bool = True                        # False: attention weights whole on every TP rank
     hc_attn: Optional["HyperConn"] = None
     hc_ffn: Optional["HyperConn"] = None
 
@@ -339,7 +340,7 @@ def _shard_ffn(gu: torch.Tensor, down: torch.Tensor, I: int, tp_rank: int, tp_si
 
 def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0, tp_size=1,
                 expert_chunk: int = 16, with_delta: bool = False, ep: bool = False,
-                expert_source=None) -> LayerWeights:
+                expert_source=None, attn_tp: bool = True) -> LayerWeights:
     """One decoder layer, sharded for rank `tp_rank` of a `tp_size` tensor-parallel
     group.  Full matrices are drawn first (the same draws for every TP size) and
     then sliced, so TP runs compute the same function as one GPU:
@@ -347,18 +348,21 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
       * dense FFN and shared expert: gate/up rows and down columns split, each
         shard zero-padded to the FP8 block;
       * routed experts: every expert's intermediate dimension split (w13 rows,
-        w2 columns), so each rank streams 1/tp of every routed expert."""
+        w2 columns), so each rank streams 1/tp of every routed expert.
+    With ``attn_tp=False`` the attention weights stay whole on every rank (replicated
+    attention: its output needs no reduction); the FFN / experts are still sharded."""
     H, dt = cfg.hidden, cfg.dense_dtype
     rng.counter = 1000 * (li + 1)      # per-layer draw stream: a layer's weights do not depend on which
     nh = cfg.num_heads                 # other layers a (pipeline) stage builds
     assert nh % tp_size == 0, "num_heads must divide by the TP size"
-    Hh = nh // tp_size
+    a_rank, a_size = (tp_rank, tp_size) if attn_tp else (0, 1)
+    Hh = nh // a_size
     qk = cfg.qk_head_dim
     nope_v = cfg.qk_nope_dim + cfg.v_head_dim
     lin = lambda w: make_linear(w, dt)  # noqa: E731
     ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=dev)  # noqa: E731
     q_lora = cfg.q_lora_rank
-    h0, h1 = tp_rank * Hh, (tp_rank + 1) * Hh
+    h0, h1 = a_rank * Hh, (a_rank + 1) * Hh
     q_b = rng.normal((nh * qk, q_lora))[h0 * qk:h1 * qk]
     kv_b = rng.normal((nh * nope_v, cfg.kv_lora_rank))[h0 * nope_v:h1 * nope_v]
     o = rng.normal((H, nh * cfg.v_head_dim))[:, h0 * cfg.v_head_dim:h1 * cfg.v_head_dim]
@@ -371,6 +375,7 @@ def _make_layer(cfg: ModelConfig, rng: _Rng, li: int, dev, moe: bool, tp_rank=0,
         kv_b=lin(kv_b.contiguous()),
         o=lin(o.contiguous()),
         ffn_norm=ones(H),
+        attn_tp=attn_tp or tp_size == 1,
     )
     if isinstance(lw.kv_b, Fp8Linear):
         lw.w_uk_t, lw.w_uv = _derive_absorb(lw.kv_b, cfg, Hh)
@@ -489,7 +494,7 @@ def pp_layer_range(num_layers: int, pp_rank: int, pp_size: int):
 def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int = 0, tp_size: int = 1,
                    with_mtp: bool = True, num_layers: Optional[int] = None, pp_rank: int = 0,
                    pp_size: int = 1, with_delta: bool = False, expert_parallel: bool = False,
-                   expert_source=None) -> ModelWeights:
+                   expert_source=None, attn_tp: bool = True) -> ModelWeights:
     """Synthetic random-init weights of the given architecture (N(0, 0.02)).
     With pp_size > 1 only the stage's layers are built; the first stage holds
     the embedding, the last the final norm, the head and the MTP module."""
@@ -502,7 +507,7 @@ def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int =
     rng.counter = 0
     embed = rng.normal((cfg.vocab, H)).to(torch.bfloat16) if first else None
     layers = [_make_layer(cfg, rng, i, dev, cfg.is_moe_layer(i), tp_rank, tp_size, with_delta=with_delta,
-                          ep=expert_parallel, expert_source=expert_source) for i in range(l0, l1)]
+                          ep=expert_parallel, expert_source=expert_source, attn_tp=attn_tp) for i in range(l0, l1)]
     head = None
     if last:
         rng.counter = 1
@@ -523,7 +528,7 @@ def random_weights(cfg: ModelConfig, device="cpu", seed: int = 0, tp_rank: int =
             hnorm=torch.ones(H, dtype=torch.bfloat16, device=dev),
             eh_proj=eh,
             layer=_make_layer(cfg, rng, L, dev, True, tp_rank, tp_size, with_delta=with_delta, ep=expert_parallel,
-                              expert_source=expert_source),
+                              expert_source=expert_source, attn_tp=attn_tp),
             head_norm=torch.ones(H, dtype=torch.bfloat16, device=dev))
     if cfg.hc_mult > 1:
         random_hyper_connections(mw, seed, L)
