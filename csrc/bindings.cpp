@@ -22,7 +22,8 @@ void router_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_
 void build_pairs(torch::Tensor topk_ids, int64_t E, int64_t MB, torch::Tensor rank_scratch,
                  torch::Tensor sorted_tok, torch::Tensor pos_of, torch::Tensor pairs, torch::Tensor n_pairs,
                  torch::Tensor status, int64_t e_lo);
-void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out);
+void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> part,
+                   c10::optional<torch::Tensor> cnt);
 void moe_route_fused(torch::Tensor x, torch::Tensor w, torch::Tensor logits, c10::optional<torch::Tensor> bias,
                      int64_t k, bool sigmoid, int64_t n_group, int64_t topk_group, bool norm, double scaling,
                      torch::Tensor ids, torch::Tensor wts, int64_t MB, torch::Tensor rank_scratch,
@@ -151,7 +152,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rank_scratch"), py::arg("sorted_tok"), py::arg("pos_of"), py::arg("pairs"), py::arg("n_pairs"),
         py::arg("n_rows"), py::arg("status"), py::arg("e_lo") = -1);
   m.def("gather_rows", &gather_rows);
-  m.def("router_logits", &router_logits);
+  m.def("router_logits", &router_logits, py::arg("x"), py::arg("w"), py::arg("out"), py::arg("part") = py::none(),
+        py::arg("cnt") = py::none());
   m.def("moe_route_fused", &moe_route_fused, py::arg("x"), py::arg("w"), py::arg("logits"), py::arg("bias"),
         py::arg("k"), py::arg("sigmoid"), py::arg("n_group"), py::arg("topk_group"), py::arg("norm"),
         py::arg("scaling"), py::arg("ids"), py::arg("wts"), py::arg("MB"), py::arg("rank_scratch"),

@@ -210,7 +210,8 @@ __global__ void router_logits_kernel(const __nv_bfloat16* __restrict__ x, int T,
 // consumed by bf16 m16n8k16 MMAs, one 16-token strip per warp.
 __global__ void __launch_bounds__(128) router_logits_mma_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
                                                                 const __nv_bfloat16* __restrict__ w, int E,
-                                                                float* __restrict__ out) {
+                                                                float* __restrict__ out, float* __restrict__ part,
+                                                                int* __restrict__ cnt, int kslice) {
   constexpr int BT = 64, BE = 64, BK = 64, LD = BK + 8;
   __shared__ __align__(16) __nv_bfloat16 sx[2][BT * LD];
   __shared__ __align__(16) __nv_bfloat16 sw[2][BE * LD];
@@ -230,17 +231,18 @@ __global__ void __launch_bounds__(128) router_logits_mma_kernel(const __nv_bfloa
       }
     }
   };
+  // K slice of this CTA (grid.z): chunks [kc0, kc0 + nk) of 64
+  const int kc0 = blockIdx.z * (kslice / BK), nk = min(kslice, H - blockIdx.z * kslice) / BK;
   // router weights are immutable: their first slice may load before the previous kernel ends
-  load(0, 0, false);
+  load(0, kc0 * BK, false);
   pdl_entry();
-  load(0, 0, true);
+  load(0, kc0 * BK, true);
   asm volatile("cp.async.commit_group;" ::: "memory");
   float acc[8][4];
 #pragma unroll
   for (int n = 0; n < 8; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-  const int nk = H / BK;
   for (int kc = 0; kc < nk; kc++) {
-    if (kc + 1 < nk) load((kc + 1) & 1, (kc + 1) * BK, true);
+    if (kc + 1 < nk) load((kc + 1) & 1, (kc0 + kc + 1) * BK, true);
     asm volatile("cp.async.commit_group;" ::: "memory");
     asm volatile("cp.async.wait_group 1;" ::: "memory");
     __syncthreads();
@@ -260,11 +262,37 @@ __global__ void __launch_bounds__(128) router_logits_mma_kernel(const __nv_bfloa
     __syncthreads();
   }
   const int r0 = t0 + warp * 16 + g;
+  const int ks = gridDim.z;
+  // one slice: straight to out; several: partials to part[z], and the tile's last CTA (arrival
+  // counter, self-resetting) adds them in slice order -- the same sum on every run and rank
+  float* dst = ks == 1 ? out : part + (size_t)blockIdx.z * T * E;
 #pragma unroll
   for (int n = 0; n < 8; n++) {
     const int col = e0 + n * 8 + 2 * t;
-    if (r0 < T) *reinterpret_cast<float2*>(out + (size_t)r0 * E + col) = make_float2(acc[n][0], acc[n][1]);
-    if (r0 + 8 < T) *reinterpret_cast<float2*>(out + (size_t)(r0 + 8) * E + col) = make_float2(acc[n][2], acc[n][3]);
+    if (r0 < T) *reinterpret_cast<float2*>(dst + (size_t)r0 * E + col) = make_float2(acc[n][0], acc[n][1]);
+    if (r0 + 8 < T) *reinterpret_cast<float2*>(dst + (size_t)(r0 + 8) * E + col) = make_float2(acc[n][2], acc[n][3]);
+  }
+  if (ks == 1) return;
+  __shared__ int last;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    int* c = cnt + blockIdx.y * gridDim.x + blockIdx.x;
+    last = atomicAdd(c, 1) == ks - 1;
+    if (last) *c = 0;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (int i = tid; i < BT * BE / 4; i += 128) {
+    const int r = t0 + (i * 4) / BE, col = e0 + (i * 4) % BE;
+    if (r >= T) continue;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int z = 0; z < ks; z++) {
+      const float4 u = __ldcg(reinterpret_cast<const float4*>(part + ((size_t)z * T + r) * E + col));
+      v.x += u.x; v.y += u.y; v.z += u.z; v.w += u.w;
+    }
+    *reinterpret_cast<float4*>(out + (size_t)r * E + col) = v;
   }
 }
 
@@ -545,17 +573,28 @@ void moe_route_fused(torch::Tensor x, torch::Tensor w, torch::Tensor logits, c10
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out) {
+void router_logits(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> part,
+                   c10::optional<torch::Tensor> cnt) {
   const int T = x.size(0), H = x.size(1), E = w.size(0);
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.is_contiguous() &&
               w.is_contiguous() && H % 256 == 0, "router_logits: bf16 contiguous, H % 256 == 0");
   if (T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  // prefill-sized T: tensor-core tiles (a 64 x 64 tile per CTA walks all of K, so decode-sized
-  // T -- a handful of CTAs -- stays on the warp-per-expert kernel, which spreads E over the GPU)
-  if (T >= 256 && E % 64 == 0 && H % 64 == 0 && out.is_contiguous()) {
-    launch_k(router_logits_mma_kernel, dim3((T + 63) / 64, E / 64), 128, 0, stream, (const __nv_bfloat16*)x.data_ptr(),
-             T, H, (const __nv_bfloat16*)w.data_ptr(), E, out.data_ptr<float>());
+  // T > 64: tensor-core tiles of 64 tokens x 64 experts; when the tiles alone would leave the
+  // GPU mostly idle (decode batches of tens of rows) K is sliced across grid.z, given scratch
+  // for the partials (part >= ks * T * E floats) and the per-tile arrival counters (zeroed)
+  if (T > 64 && E % 64 == 0 && H % 64 == 0 && out.is_contiguous()) {
+    const int tiles = ((T + 63) / 64) * (E / 64);
+    int ks = 1;
+    const bool have = part.has_value() && part->defined() && cnt.has_value() && cnt->defined();
+    if (have) {
+      ks = std::max(1, std::min(H / 512, 64 / tiles));   // ~64 CTAs: short K loops, an 8-slice sum
+      while (ks > 1 && ((int64_t)ks * T * E > part->numel() || (H / 64) % ks)) ks--;
+      TORCH_CHECK(cnt->numel() >= tiles, "router_logits: counters");
+    }
+    launch_k(router_logits_mma_kernel, dim3((T + 63) / 64, E / 64, ks), 128, 0, stream,
+             (const __nv_bfloat16*)x.data_ptr(), T, H, (const __nv_bfloat16*)w.data_ptr(), E, out.data_ptr<float>(),
+             ks > 1 ? part->data_ptr<float>() : nullptr, ks > 1 ? cnt->data_ptr<int>() : nullptr, H / ks);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return;
   }

@@ -472,7 +472,7 @@ def test_rmsnorm_quant_output_stride(C):
     assert torch.equal(q[:, H:], qa) and torch.equal(s[:, H // 64:], sa)
 
 
-@pytest.mark.parametrize("T,E", [(1, 256), (3, 256), (20, 256), (96, 256), (1000, 384), (300, 64)])
+@pytest.mark.parametrize("T,E", [(1, 256), (3, 256), (20, 256), (96, 256), (192, 384), (1000, 384), (300, 64)])
 def test_router_logits(C, T, E):
     """Decode-sized (warp per expert) and prefill-sized (tensor-core tiles, T > 64) router
     logits against the fp32 product of the same bf16 operands."""
@@ -483,6 +483,14 @@ def test_router_logits(C, T, E):
     out = torch.empty(T, E, device=DEV)
     C.router_logits(x.to(DEV), w.to(DEV), out)
     assert rel(out.cpu(), x.float() @ w.float().t()) < 1e-5
+    if 64 < T <= 512:      # K-sliced tiles with the in-kernel ordered reduction: same result, twice
+        part = torch.empty(16 * T * E, device=DEV)
+        cnt = torch.zeros(64, dtype=torch.int32, device=DEV)
+        o2 = torch.empty(T, E, device=DEV)
+        for _ in range(2):
+            C.router_logits(x.to(DEV), w.to(DEV), o2, part, cnt)
+            assert rel(o2.cpu(), x.float() @ w.float().t()) < 1e-5
+        assert int(cnt.abs().sum()) == 0
 
 
 @pytest.mark.parametrize("R,V", [(1, 129280), (7, 4096), (3, 100)])

@@ -216,6 +216,17 @@ class NativeRunner:
         torch.distributed.all_gather_into_tensor(allmv, mv, group=self.tp_group)
         self.C.argmax_merge(allmv, ids)
 
+    def _router_logits(self, hb, lw, logits):
+        """Router logits; decode-sized batches (up to 512 rows) give the kernel scratch for
+        K-sliced partials and per-tile counters, so tens of rows still fill the GPU."""
+        T, E = logits.shape
+        if 64 < T <= 512:
+            part = self.ws.get("router.part", (16 * T * E,), torch.float32)
+            cnt = self.ws.zeros("router.cnt", (64,), torch.int32)
+            self.C.router_logits(hb, self._router_w(lw), logits, part, cnt)
+        else:
+            self.C.router_logits(hb, self._router_w(lw), logits)
+
     def _router_w(self, lw):
         w = getattr(lw, "_router_w_bf16", None)
         if w is None:
@@ -665,7 +676,7 @@ class NativeRunner:
         topp = self.ecfg.moet.topp
         if self.ep is not None:
             # DP attention + EP: route over all experts, then the all-to-all around the owners' kernels
-            C.router_logits(hb, self._router_w(lw), logits)
+            self._router_logits(hb, lw, logits)
             C.router_topk(logits, lw.router_bias, k, cfg.router == "sigmoid", cfg.n_group, cfg.topk_group,
                           cfg.norm_topk_prob, cfg.routed_scaling, ids, wts)
             fused = ctx.mode == "decode" and R <= self.ep.cap and ctx.mb in (8, 16, 32)
@@ -698,7 +709,7 @@ class NativeRunner:
             y2 = self._moe_gemv_pairs(h2q, h2s, stok, pairs, npairs, ex, R, MB, mli)
         else:
             # bf16 operands, fp32 accumulation; prefill-sized T runs on tensor-core tiles
-            C.router_logits(hb, self._router_w(lw), logits)
+            self._router_logits(hb, lw, logits)
             C.router_topk(logits, lw.router_bias, k, cfg.router == "sigmoid", cfg.n_group, cfg.topk_group,
                           cfg.norm_topk_prob, cfg.routed_scaling, ids, wts)
             if topp > 0:        # expert top-p pruning: the tail moves to the top-1 expert with weight 0
