@@ -257,8 +257,10 @@ def main():
             "config": {"model": "ds4-flash-shape (32 layers, hidden 4096, 256 experts top-8, MLA, MTP k=2)",
                        "global_batch": world if args.ep else 1, "seq_len": args.prompt_len,
                        "parallelism": (f"dp{world} attention + ep{world} experts (peer-memory all-to-all)" if args.ep
-                                       else (f"tp{world} (fused peer-memory all-reduce)" if llm.runner.ar is not None
-                                             else f"tp{world} (NCCL all-reduce)") if world > 1 else "single"),
+                                       else (f"tp{world} (" + ("fused peer-memory" if llm.runner.ar is not None
+                                                               else "NCCL") + " all-reduce; attention "
+                                             + ("replicated" if not llm.mw.layers[0].attn_tp else "head-sharded")
+                                             + ", experts / FFN / vocab sharded)") if world > 1 else "single"),
                        "l2": "inputs larger than L2 (each step streams ~7 GB of weights)",
                        "layers": args.layers or 32},
             "mtp_acceptance_per_step": round(acc, 4), "steps_per_s": round(1000.0 / ms, 2),
