@@ -52,6 +52,8 @@ def main():
     ap.add_argument("--sp", type=int, default=0,
                     help="sequence-parallel prefill of one prompt of this many tokens over the N ranks "
                          "(replicated weights); reports prefill tok/s, device-timed, max over ranks")
+    ap.add_argument("--sp-chunk", type=int, default=0,
+                    help="--sp on one GPU: prefill the prompt in chunks of this many tokens (block-aligned)")
     ap.add_argument("--expert-cache-gb", type=float, default=0.0,
                     help="residency: serve routed experts from a GPU cache of this many GiB over a host store "
                          "(reports 1-stream decode through LLM.generate, host fetches included)")
@@ -303,8 +305,18 @@ def _sp_prefill(args, world, rank, local, dist):
     bt = [0] * llm.max_blocks
     bt[:len(blocks)] = blocks
     st.block_table[0, :len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
-    run = (lambda: llm.runner.prefill_sp(prompt, bt, 0, st)) if world > 1 else \
-        (lambda: llm.runner.prefill([prompt], [bt], [0], st))
+    C = args.sp_chunk
+
+    def chunked():      # one GPU, chunks of C tokens: every chunk after the first reads cached positions
+        for lo in range(0, n - C, C):
+            llm.runner.prefill_chunk(prompt, bt, lo, min(n, lo + C))
+        return llm.runner.prefill([prompt], [bt], [0], st, starts=[(n - 1) // C * C])
+    if world > 1:
+        run = lambda: llm.runner.prefill_sp(prompt, bt, 0, st)     # noqa: E731
+    elif C:
+        run = chunked
+    else:
+        run = lambda: llm.runner.prefill([prompt], [bt], [0], st)   # noqa: E731
     for _ in range(max(1, args.warmup - 2)):
         run()
     times = []
@@ -327,7 +339,7 @@ def _sp_prefill(args, world, rank, local, dist):
                           "value": round(n * 1000.0 / ms, 1), "unit": "tok/s", "n_gpus": world, "prompt_tokens": n,
                           "ms": round(ms, 2), "higher_is_better": True, "scaling": "strong",
                           "parallelism": f"sp{world} (replicated weights, per-layer cache all-gather)" if world > 1
-                          else "single", "first_token": int(first) if not hasattr(first, "tolist") else
+                          else (f"single, {C}-token chunks" if C else "single"), "first_token": int(first) if not hasattr(first, "tolist") else
                           int(first.tolist()[0]), "dtype": "bf16 activations; fp8 dense; 2-bit experts",
                           "data": "synthetic prompt, random-init weights"}), flush=True)
     if world > 1:

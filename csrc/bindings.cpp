@@ -103,7 +103,7 @@ void kv_prep(torch::Tensor kva, int64_t lat, int64_t rope, torch::Tensor norm_w,
 // mla_prefill.cu
 void mla_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kr, torch::Tensor cu_seqlens, int64_t max_len,
                  double scale, c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_s,
-                 c10::optional<torch::Tensor> out_bf16);
+                 c10::optional<torch::Tensor> out_bf16, c10::optional<torch::Tensor> cu_seqlens_k);
 // quant_pack.cu
 void nvfp4_quant(torch::Tensor w, double ts, torch::Tensor packed, torch::Tensor sf);
 void w2_quant_pack(torch::Tensor packed, torch::Tensor sf, double ts, int64_t zero_mode, torch::Tensor codes_plane,
@@ -202,7 +202,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_combine", &mla_combine);
   m.def("q_prep", &q_prep);
   m.def("kv_prep", &kv_prep);
-  m.def("mla_prefill", &mla_prefill);
+  m.def("mla_prefill", &mla_prefill, py::arg("q"), py::arg("kvb"), py::arg("kr"), py::arg("cu_seqlens"),
+        py::arg("max_len"), py::arg("scale"), py::arg("out_q"), py::arg("out_s"), py::arg("out_bf16"),
+        py::arg("cu_seqlens_k") = py::none());
   m.def("nvfp4_quant", &nvfp4_quant);
   m.def("w2_quant_pack", &w2_quant_pack);
   m.def("argmax_lse", &argmax_lse);

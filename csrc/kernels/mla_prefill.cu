@@ -3,7 +3,10 @@
 // DN = 128 / DV = 128 (DeepSeek-V4 shape) or DN = 192 / DV = 256 (GLM-5.x shape).
 // A CTA accumulates 128 value columns; with DV = 256 two CTAs share a head (each
 // recomputes Q.K^T), which keeps the O accumulator at 64 registers per thread.
-// Causal within each sequence of a varlen batch (cu_seqlens).  Flash-attention
+// Causal within each sequence of a varlen batch (cu_seqlens).  With a separate key
+// batch (cu_seqlens_k) sequence i's nq queries are its LAST nq positions: query j sits at
+// position nk - nq + j and sees keys [0, nk - nq + j] -- a chunk of a long prompt whose
+// earlier positions' K/V come from the cache.  Flash-attention
 // structure: a CTA owns 128 query rows of one head (8 warps x 16 rows), Q
 // fragments stay in registers, K/V tiles of 64 keys are double-buffered in
 // shared memory with cp.async, softmax is online in registers, P is reused
@@ -31,7 +34,7 @@ struct PrefillArgs {
   const __nv_bfloat16* q; long long q_tok_stride; int q_head_stride;     // [T, Hh, DN + 64]
   const __nv_bfloat16* kvb; long long kvb_tok_stride; int kvb_head_stride; // [T, Hh, DN + DV] = k_nope | v
   const __nv_bfloat16* kr; long long kr_tok_stride;                      // [T, 64]
-  const int* cu_seqlens; int nseq;
+  const int* cu_seqlens; const int* cu_seqlens_k; int nseq;   // cu_seqlens_k null: keys = queries
   int Hh, DV;
   float scale_log2;
   uint8_t* out_q; uint8_t* out_s; __nv_bfloat16* out_bf16;   // [T, Hh*DV]
@@ -48,9 +51,12 @@ __global__ void __launch_bounds__(256, 1) mla_prefill_kernel(PrefillArgs p) {
   const int nvc = p.DV / kDV;
   const int qtile = blockIdx.x, h = blockIdx.y / nvc, vc = blockIdx.y % nvc, sq = blockIdx.z;
   const int vcol0 = vc * kDV;                                         // this CTA's value columns
-  const int s0 = p.cu_seqlens[sq], n = p.cu_seqlens[sq + 1] - s0;
+  const int s0 = p.cu_seqlens[sq], n = p.cu_seqlens[sq + 1] - s0;          // queries
+  const int* cuk = p.cu_seqlens_k ? p.cu_seqlens_k : p.cu_seqlens;
+  const int sk0 = cuk[sq], nk = cuk[sq + 1] - sk0;                         // keys
+  const int off = nk - n;                                                  // position of query 0
   const int q0 = qtile * kBQ;
-  if (q0 >= n) return;
+  if (q0 >= n || off < 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
 
   // Q tile -> smem
@@ -68,20 +74,20 @@ __global__ void __launch_bounds__(256, 1) mla_prefill_kernel(PrefillArgs p) {
     for (int i = threadIdx.x; i < kBK * (kD / 8); i += blockDim.x) {
       const int r = i / (kD / 8), c = (i % (kD / 8)) * 8;
       const int tok = k0 + r;
-      const int tt = s0 + min(tok, n - 1);
+      const int tt = sk0 + min(tok, nk - 1);
       const __nv_bfloat16* src = c < kDN ? p.kvb + (size_t)tt * p.kvb_tok_stride + (size_t)h * p.kvb_head_stride + c
                                          : p.kr + (size_t)tt * p.kr_tok_stride + (c - kDN);
-      cp_async16(kd + r * kKS + c, src, tok < n);
+      cp_async16(kd + r * kKS + c, src, tok < nk);
     }
     for (int i = threadIdx.x; i < kBK * (kDV / 8); i += blockDim.x) {
       const int r = i / (kDV / 8), c = (i % (kDV / 8)) * 8;
       const int tok = k0 + r;
-      const int tt = s0 + min(tok, n - 1);
+      const int tt = sk0 + min(tok, nk - 1);
       cp_async16(vd + r * kVS + c,
-                 p.kvb + (size_t)tt * p.kvb_tok_stride + (size_t)h * p.kvb_head_stride + kDN + vcol0 + c, tok < n);
+                 p.kvb + (size_t)tt * p.kvb_tok_stride + (size_t)h * p.kvb_head_stride + kDN + vcol0 + c, tok < nk);
     }
   };
-  const int nkt = min((q0 + kBQ + kBK - 1) / kBK, (n + kBK - 1) / kBK);
+  const int nkt = min((off + q0 + kBQ + kBK - 1) / kBK, (nk + kBK - 1) / kBK);
   load_kv(0, 0);
   cp_async_commit();
   cp_async_wait<1>();
@@ -96,7 +102,8 @@ __global__ void __launch_bounds__(256, 1) mla_prefill_kernel(PrefillArgs p) {
 #pragma unroll
   for (int i = 0; i < kDV / 8; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-  const int qrow0 = q0 + warp * 16 + g, qrow1 = qrow0 + 8;
+  const int qrow0 = q0 + warp * 16 + g, qrow1 = qrow0 + 8;      // query rows (epilogue)
+  const int kpos0 = off + qrow0, kpos1 = kpos0 + 8;               // their positions (causal mask)
 
   for (int kt = 0; kt < nkt; kt++) {
     const int buf = kt & 1;
@@ -108,7 +115,7 @@ __global__ void __launch_bounds__(256, 1) mla_prefill_kernel(PrefillArgs p) {
     const __nv_bfloat16* vb = Vs + buf * kBK * kVS;
     const int k0 = kt * kBK;
     // skip fully-masked tiles for this warp's rows
-    const bool warp_active = k0 <= q0 + warp * 16 + 15;
+    const bool warp_active = k0 <= off + q0 + warp * 16 + 15;
     if (warp_active) {
       float s[kBK / 8][4];
 #pragma unroll
@@ -130,10 +137,10 @@ __global__ void __launch_bounds__(256, 1) mla_prefill_kernel(PrefillArgs p) {
 #pragma unroll
       for (int i = 0; i < kBK / 8; i++) {
         const int kc = k0 + i * 8 + 2 * t;
-        s[i][0] = (kc <= qrow0 && kc < n) ? s[i][0] * p.scale_log2 : -INFINITY;
-        s[i][1] = (kc + 1 <= qrow0 && kc + 1 < n) ? s[i][1] * p.scale_log2 : -INFINITY;
-        s[i][2] = (kc <= qrow1 && kc < n) ? s[i][2] * p.scale_log2 : -INFINITY;
-        s[i][3] = (kc + 1 <= qrow1 && kc + 1 < n) ? s[i][3] * p.scale_log2 : -INFINITY;
+        s[i][0] = (kc <= kpos0 && kc < nk) ? s[i][0] * p.scale_log2 : -INFINITY;
+        s[i][1] = (kc + 1 <= kpos0 && kc + 1 < nk) ? s[i][1] * p.scale_log2 : -INFINITY;
+        s[i][2] = (kc <= kpos1 && kc < nk) ? s[i][2] * p.scale_log2 : -INFINITY;
+        s[i][3] = (kc + 1 <= kpos1 && kc + 1 < nk) ? s[i][3] * p.scale_log2 : -INFINITY;
         mx0 = fmaxf(mx0, fmaxf(s[i][0], s[i][1]));
         mx1 = fmaxf(mx1, fmaxf(s[i][2], s[i][3]));
       }
@@ -231,7 +238,7 @@ using namespace moet;
 
 void mla_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kr, torch::Tensor cu_seqlens, int64_t max_len,
                  double scale, c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_s,
-                 c10::optional<torch::Tensor> out_bf16) {
+                 c10::optional<torch::Tensor> out_bf16, c10::optional<torch::Tensor> cu_seqlens_k) {
   const int Hh = q.size(1);
   const int DN = q.size(2) - 64, DV = kvb.size(2) - DN;
   TORCH_CHECK((DN == 128 || DN == 192) && q.stride(2) == 1, "mla_prefill: q [T, Hh, 192 | 256] (nope 128 | 192 + rope 64)");
@@ -244,6 +251,12 @@ void mla_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kr, torch::Te
   p.kvb = (const __nv_bfloat16*)kvb.data_ptr(); p.kvb_tok_stride = kvb.stride(0); p.kvb_head_stride = kvb.stride(1);
   p.kr = (const __nv_bfloat16*)kr.data_ptr(); p.kr_tok_stride = kr.stride(0);
   p.cu_seqlens = cu_seqlens.data_ptr<int>(); p.nseq = nseq; p.Hh = Hh; p.DV = DV;
+  p.cu_seqlens_k = nullptr;
+  if (cu_seqlens_k.has_value() && cu_seqlens_k->defined()) {
+    TORCH_CHECK(cu_seqlens_k->numel() == nseq + 1 && cu_seqlens_k->scalar_type() == at::kInt && cu_seqlens_k->is_cuda(),
+                "mla_prefill: cu_seqlens_k [nseq + 1] int32 on the device");
+    p.cu_seqlens_k = cu_seqlens_k->data_ptr<int>();
+  }
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.out_q = (uint8_t*)opt_ptr(out_q); p.out_s = (uint8_t*)opt_ptr(out_s); p.out_bf16 = (__nv_bfloat16*)opt_ptr(out_bf16);
   auto stream = at::cuda::getCurrentCUDAStream();

@@ -19,6 +19,10 @@ class Stub:
         self.ws = types.SimpleNamespace(get=lambda name, shape, dtype: torch.zeros(shape, dtype=dtype))
         self.C = types.SimpleNamespace(rmsnorm_quant=lambda *a: None)
         self.ws_prefill = self.ws
+        self.cached_flash_min = 1
+
+    def _key_rows(self, ctx, ends):
+        return NativeRunner._key_rows(self, ctx, ends)
 
     def _main(self, toks, ctx):
         self.calls.append(("main", toks.clone(), ctx))
@@ -60,6 +64,10 @@ def test_cached_prefill_rows_and_slots():
     assert (ctx.slot // KV_BLOCK).tolist() == blocks and (ctx.slot % KV_BLOCK).tolist() == [p % KV_BLOCK for p in ctx.pos.tolist()]
     assert nxt.tolist() == p0[64:] + [7] + p1[1:] + [7]          # the first generated token closes each prompt
     assert first.tolist() == [7, 7] and st.seq_pos.tolist() == [80, 30]
+    # flash path: every key row of each sequence (cached prefix + suffix), in position order
+    assert ctx.cu_k.tolist() == [0, 80, 110]
+    want = [bt[0][q // KV_BLOCK] * KV_BLOCK + q % KV_BLOCK for q in range(80)] + [7 * KV_BLOCK + q for q in range(30)]
+    assert ctx.kv_idx.tolist() == want
     assert st.tokens[:, 0].tolist() == [7, 7] and st.tokens[:, 1].tolist() == [9, 9]
 
 
@@ -71,6 +79,12 @@ def test_prefill_chunk_rows():
     assert ctx.mode == "cached" and toks.tolist() == p[40:70] and ctx.pos.tolist() == list(range(40, 70))
     assert nxt.tolist() == p[41:71]                                # every MTP row's next token is a prompt token
     assert (ctx.slot // KV_BLOCK).tolist() == [3 if q < 64 else 4 for q in range(40, 70)]
+    assert ctx.cu_k.tolist() == [0, 70]
+    assert ctx.kv_idx.tolist() == [(3 if q < 64 else 4) * KV_BLOCK + q % KV_BLOCK for q in range(70)]
+    r.cached_flash_min = 31              # a 30-row chunk stays on absorbed attention
+    r.calls.clear()
+    NativeRunner.prefill_chunk(r, p, [3, 4, 0, 0], 40, 70)
+    assert r.calls[0][2].kv_idx is None
     r.calls.clear()
     NativeRunner.prefill_chunk(r, p, [3, 4, 0, 0], 0, 16)
     assert r.calls[0][2].mode == "prefill" and r.calls[0][2].cu_seqlens.tolist() == [0, 16]

@@ -345,6 +345,39 @@ def test_mla_prefill(C, lens, Hh):
     assert rel(deq, out.cpu().float()) < 5e-2
 
 
+@pytest.mark.parametrize("qlens,klens,Hh", [([64], [200], 2), ([130, 1, 70], [130, 300, 200], 3)])
+def test_mla_prefill_query_offset(C, qlens, klens, Hh):
+    """Separate key batch: sequence i's queries are its last qlens[i] positions of klens[i]
+    keys (a prompt chunk over cached positions); kr is a strided view, as when it is the
+    rope tail of gathered cache rows."""
+    g = torch.Generator().manual_seed(sum(qlens) + sum(klens))
+    T, Nk = sum(qlens), sum(klens)
+    q = (torch.randn(T, Hh, 192, generator=g) * 0.5).to(torch.bfloat16)
+    kvb = (torch.randn(Nk, Hh, 256, generator=g) * 0.5).to(torch.bfloat16)
+    rows = (torch.randn(Nk, 584, generator=g) * 0.5).to(torch.bfloat16)
+    cu = torch.tensor([0] + torch.tensor(qlens).cumsum(0).tolist(), dtype=torch.int32)
+    cuk = torch.tensor([0] + torch.tensor(klens).cumsum(0).tolist(), dtype=torch.int32)
+    out = torch.empty(T, Hh * 128, dtype=torch.bfloat16, device=DEV)
+    oq = torch.empty(T, Hh * 128, dtype=torch.uint8, device=DEV); os_ = torch.empty(T, Hh * 2, dtype=torch.uint8, device=DEV)
+    scale = 1 / math.sqrt(192)
+    rows_d = rows.to(DEV)
+    C.mla_prefill(q.to(DEV), kvb.to(DEV), rows_d[:, 512:576], cu.to(DEV), max(qlens), scale, oq, os_, out,
+                  cu_seqlens_k=cuk.to(DEV))
+    kr = rows[:, 512:576]
+    for si, (n, nk) in enumerate(zip(qlens, klens)):
+        s0, k0, off = int(cu[si]), int(cuk[si]), nk - n
+        for h in range(Hh):
+            qq = q[s0:s0 + n, h].float()
+            kk = torch.cat([kvb[k0:k0 + nk, h, :128].float(), kr[k0:k0 + nk].float()], -1)
+            vv = kvb[k0:k0 + nk, h, 128:].float()
+            s = (qq @ kk.t()) * scale
+            mask = torch.arange(nk)[None, :] > (off + torch.arange(n))[:, None]
+            ref = torch.softmax(s.masked_fill(mask, float("-inf")), -1) @ vv
+            assert rel(out[s0:s0 + n, h * 128:(h + 1) * 128].cpu().float(), ref) < 2e-2, (si, h)
+    deq = fp8.dequant_act_fp8(oq.cpu().view(torch.float8_e4m3fn), os_.cpu())
+    assert rel(deq, out.cpu().float()) < 5e-2
+
+
 def test_kv_prep_bf16_and_nvfp4(C):
     g = torch.Generator().manual_seed(11)
     T = 5

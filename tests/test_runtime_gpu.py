@@ -293,3 +293,27 @@ def test_chunked_prefill_matches_full_prefill():
     r = _oracle_last_logits(ch, p)
     e_chunked, e_full = _rel(lg_chunked, r), _rel(lg_full, r)
     assert e_chunked < 0.08 and e_chunked <= e_full + 0.03, (e_chunked, e_full)
+
+
+@pytest.mark.parametrize("flash_min", [128, 1 << 30])
+def test_chunked_prefill_flash_and_absorbed_paths(flash_min):
+    """Chunks of 128 rows over cached positions: with the flash path (key rows gathered from
+    the cache, W_kv_b applied, flash kernel with the queries at the end of each key range)
+    and with absorbed attention over the paged cache, the last logits track the fp32
+    oracle as closely as one full prefill does."""
+    ch = LLM(small_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=1024, max_num_seqs=4,
+             enable_chunked_prefill=True, max_num_batched_tokens=128)
+    ch.runner.cached_flash_min = flash_min
+    p = _prompt(400, 41)
+    sp = SamplingParams(max_tokens=4, ignore_eos=True)
+    got = ch.generate([p], sp)[0].outputs[0].token_ids
+    lg = ch.runner.ws_prefill.bufs[("main.logits", torch.float32)][: ch.cfg.vocab].clone()
+    assert len(ch._chunk_log) == 4 and len(got) == 4
+    assert (("kvbk", torch.bfloat16) in ch.runner.ws_prefill.bufs) == (flash_min == 128)
+    full = LLM(small_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=1024, max_num_seqs=4)
+    want = full.generate([p], sp)[0].outputs[0].token_ids
+    lg_full = full.runner.ws_prefill.bufs[("main.logits", torch.float32)][: full.cfg.vocab].clone()
+    r = _oracle_last_logits(ch, p)
+    e, e_full = _rel(lg, r), _rel(lg_full, r)
+    assert e < 0.1 and e <= e_full + 0.03, (e, e_full)
+    assert got[0] == want[0] or float(r[got[0]]) >= float(r.max()) - 0.3

@@ -76,6 +76,10 @@ class StepCtx:
     cu_seqlens: Optional[torch.Tensor] = None
     max_len: int = 0
     mb: int = 8                  # rows per expert pair
+    # "cached" mode on the flash path: cache slots of every key row (sequence i's positions
+    # [0, end_i)) and their cu_seqlens; None = attention reads the paged cache (absorbed)
+    kv_idx: Optional[torch.Tensor] = None
+    cu_k: Optional[torch.Tensor] = None
 
 
 class NativeRunner:
@@ -142,6 +146,9 @@ class NativeRunner:
         self.timers = None          # SpanTimers of prefill components (VLLM_PREFILL_TIMERS_FLUSH)
         # token count from which dense linears run on the tcgen05 GEMM (128-token tiles)
         self.tc_min_t = int(os.environ.get("MOET_TC_MIN_T", "16"))
+        # "cached" chunks of at least this many rows run the flash prefill kernel over key
+        # rows gathered from the cache (W_kv_b applied to them) instead of absorbed attention
+        self.cached_flash_min = int(os.environ.get("MOET_CACHED_FLASH_MIN", "128"))
         # decode expert tiles: 8-token pairs up to this many routed rows, 16-token pairs above
         self.mb8_max_r = int(os.environ.get("MOET_MB8_MAX_R", "2048"))
         # decode experts on the tcgen05 kernel with this token tile (0: mma.sync GEMV)
@@ -556,7 +563,10 @@ class NativeRunner:
         else:
             self._norm_in(x, lw.attn_norm, None, hq, hs)
             self._gemv(hq, hs, lw.qkv_a, qkva)
-        absorbed = ctx.mode in ("decode", "cached")     # attention reads the paged latent cache
+        # attention reads the paged latent cache (absorbed) unless this "cached" chunk has
+        # key rows to gather for the flash kernel (dense attention, bf16 cache)
+        flash_cached = ctx.mode == "cached" and ctx.kv_idx is not None and lw.idx_wq is None and self.kv_mode == 1
+        absorbed = ctx.mode == "decode" or (ctx.mode == "cached" and not flash_cached)
         if absorbed:
             with self._fork():     # latent KV path (norm, rope, cache write) beside the query path
                 C.kv_prep(qkva[:, ql:], lat, rope, lw.kv_a_norm, cfg.rms_eps, ctx.pos, self.cos_sin, ctx.slot,
@@ -584,6 +594,24 @@ class NativeRunner:
             C.mla_decode(qcat, cache, ctx.block_table, ctx.seq, ctx.pos, opart, mlp, self.scale, self.status, sel)
             # split merge + W_uv + e4m3 quantisation in one kernel
             C.mla_combine_uv(opart, mlp, lw.w_uv.w, lw.w_uv.s, ovq, ovs)
+        elif flash_cached:
+            # a chunk over cached positions: write its rows, then gather every key row of its
+            # sequences (cached prefix + the chunk) from the cache, quantise the latents, apply
+            # W_kv_b and run the flash kernel with the queries at the end of each key range
+            C.kv_prep(qkva[:, ql:], lat, rope, lw.kv_a_norm, cfg.rms_eps, ctx.pos, self.cos_sin, ctx.slot,
+                      self.kv_mode, cache, None, None, None, None, self.status)
+            self._sp_gather(self.kv, li)      # SP prefill: the other ranks' chunks of this layer's cache
+            Nk = ctx.kv_idx.numel()
+            rows = self.ws.get("krows", (Nk, BF16_ROW), torch.bfloat16)
+            torch.index_select(cache.view(-1, BF16_ROW), 0, ctx.kv_idx, out=rows)
+            latq, lats = self._fp8("latk", Nk, lat)
+            C.quant_fp8(rows[:, :lat], 0, latq, lats)
+            kvb = self.ws.get("kvbk", (Nk, Hh * (nope + vd)), torch.bfloat16)
+            self._gemv(latq, lats, lw.kv_b, kvb)
+            qf = self.ws.get("qfull", (T, Hh, nope + rope), torch.bfloat16)
+            C.q_prep(qb, Hh, nope, rope, ctx.pos, self.cos_sin, None, None, None, 0, qf)
+            C.mla_prefill(qf, kvb.view(Nk, Hh, nope + vd), rows[:, lat:lat + rope], ctx.cu_seqlens, ctx.max_len,
+                          self.scale, ovq, ovs, None, cu_seqlens_k=ctx.cu_k)
         else:
             latq, lats = self._fp8("lat", T, lat)
             kr = self.ws.get("kr", (T, rope), torch.bfloat16)
@@ -929,6 +957,8 @@ class NativeRunner:
         cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
         ctx = StepCtx(T=T, pos=pos, seq=seq, slot=slot, block_table=bt, mode="cached" if start else "prefill",
                       cu_seqlens=cu, max_len=T, mb=32)
+        if start:
+            self._key_rows(ctx, [end])
         x = self._main(toks, ctx)
         if self.last_stage and self.k:
             hid_all = self.ws.get("pf.hid", (T, self.cfg.hidden), torch.bfloat16)
@@ -937,6 +967,18 @@ class NativeRunner:
             nxt = torch.tensor(prompt[start + 1:end + 1], dtype=torch.int32, device=dev)
             self._mtp(hid_all, nxt, ctx, rows=torch.tensor([T - 1], device=dev))
         self.check_status("prefill chunk")
+
+    def _key_rows(self, ctx: StepCtx, ends: list):
+        """Give a "cached" step of at least `cached_flash_min` rows the flash path: the cache
+        slots of sequence i's positions [0, ends[i]) and their cu_seqlens (queries are the
+        last rows of each range)."""
+        if ctx.T < self.cached_flash_min:
+            return
+        bt = ctx.block_table
+        seq = torch.cat([torch.full((n,), i, dtype=torch.long) for i, n in enumerate(ends)]).to(self.dev)
+        pos = torch.cat([torch.arange(n, dtype=torch.long) for n in ends]).to(self.dev)
+        ctx.kv_idx = bt[seq, pos // KV_BLOCK].long() * KV_BLOCK + pos % KV_BLOCK
+        ctx.cu_k = torch.tensor([0] + list(torch.tensor(ends).cumsum(0)), dtype=torch.int32, device=self.dev)
 
     def copy_block(self, src: int, dst: int):
         """Copy one KV block (every layer's latent cache, the MTP layer's and the indexer's):
@@ -982,6 +1024,8 @@ class NativeRunner:
         cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=dev)
         ctx = StepCtx(T=T, pos=pos, seq=seq, slot=slot, block_table=bt,
                       mode="cached" if any(starts) else "prefill", cu_seqlens=cu, max_len=max(lens), mb=32)
+        if any(starts):
+            self._key_rows(ctx, full)
         x = self._main(toks, ctx)
         B = len(prompts)
         if not self.last_stage:     # the last stage computes the first tokens and drafts, then broadcasts them
