@@ -104,6 +104,12 @@ void kv_prep(torch::Tensor kva, int64_t lat, int64_t rope, torch::Tensor norm_w,
 void mla_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kr, torch::Tensor cu_seqlens, int64_t max_len,
                  double scale, c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_s,
                  c10::optional<torch::Tensor> out_bf16, c10::optional<torch::Tensor> cu_seqlens_k);
+// hyper_conn.cu
+void hc_mix(torch::Tensor xs, c10::optional<torch::Tensor> upd, c10::optional<torch::Tensor> post,
+            c10::optional<torch::Tensor> comb, c10::optional<torch::Tensor> fn, c10::optional<torch::Tensor> part);
+void hc_apply(torch::Tensor xs, torch::Tensor part, torch::Tensor base, torch::Tensor scale, double eps,
+              int64_t iters, double rms_eps, torch::Tensor h, c10::optional<torch::Tensor> post,
+              c10::optional<torch::Tensor> comb);
 // quant_pack.cu
 void nvfp4_quant(torch::Tensor w, double ts, torch::Tensor packed, torch::Tensor sf);
 void w2_quant_pack(torch::Tensor packed, torch::Tensor sf, double ts, int64_t zero_mode, torch::Tensor codes_plane,
@@ -202,6 +208,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_combine", &mla_combine);
   m.def("q_prep", &q_prep);
   m.def("kv_prep", &kv_prep);
+  m.def("hc_mix", &hc_mix, py::arg("xs"), py::arg("upd") = py::none(), py::arg("post") = py::none(),
+        py::arg("comb") = py::none(), py::arg("fn") = py::none(), py::arg("part") = py::none());
+  m.def("hc_apply", &hc_apply, py::arg("xs"), py::arg("part"), py::arg("base"), py::arg("scale"), py::arg("eps"),
+        py::arg("iters"), py::arg("rms_eps"), py::arg("h"), py::arg("post") = py::none(), py::arg("comb") = py::none());
   m.def("mla_prefill", &mla_prefill, py::arg("q"), py::arg("kvb"), py::arg("kr"), py::arg("cu_seqlens"),
         py::arg("max_len"), py::arg("scale"), py::arg("out_q"), py::arg("out_s"), py::arg("out_bf16"),
         py::arg("cu_seqlens_k") = py::none());

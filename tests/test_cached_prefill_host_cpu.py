@@ -20,6 +20,7 @@ class Stub:
         self.C = types.SimpleNamespace(rmsnorm_quant=lambda *a: None)
         self.ws_prefill = self.ws
         self.cached_flash_min = 1
+        self.hcn = 1
 
     def _key_rows(self, ctx, ends):
         return NativeRunner._key_rows(self, ctx, ends)

@@ -34,6 +34,19 @@ BF16_ROW = 584      # bf16 elements per cache row (512 latent + 64 rope + 8 pad)
 NVFP4_ROW = 352     # bytes per NVFP4 row
 
 
+def _split_cols(lin, k0: int, k1: int):
+    """Columns [k0, k1) of a linear (input features) as a linear of its own (contiguous);
+    FP8 weights split on their 128-column scale blocks."""
+    from ..models.weights import Fp8Linear, FloatLinear
+    if isinstance(lin, Fp8Linear):
+        if k0 % 128 or k1 % 128:
+            raise ValueError("FP8 column split on 128-column blocks")
+        return Fp8Linear(lin.w[:, k0:k1].contiguous(), lin.s[:, k0 // 128:k1 // 128].contiguous())
+    if isinstance(lin, FloatLinear):
+        return FloatLinear(lin.w[:, k0:k1].contiguous())
+    raise NotImplementedError(f"column split of {type(lin).__name__}")
+
+
 class Workspace:
     """Grow-only named device buffers; frozen once a graph has been captured."""
 
@@ -133,6 +146,7 @@ class NativeRunner:
         self._pend_add = None     # (residual, reduced partial, out): decode residual add left to the next norm
         self._decode = False
         self._fused = False
+        self._init_hyper_connections()
         # pipeline parallelism: this stage's layers; first stage embeds, last stage owns head + MTP
         self.pp_group = None
         self.pp_rank, self.pp_size = mw.extra.get("pp_rank", 0), mw.extra.get("pp_size", 1)
@@ -532,8 +546,11 @@ class NativeRunner:
             torch.cuda.current_stream().wait_stream(self._side)
 
     # ------------------------------------------------------------------ layer
-    def _attention(self, lw: LayerWeights, x, ctx: StepCtx, cache, li, out):
+    def _attention(self, lw: LayerWeights, x, ctx: StepCtx, cache, li, out, resid=None):
+        """out = resid + attention(norm(x)); resid defaults to x (a zero buffer under
+        hyper-connections, whose streams take the block output)."""
         cfg, C, T, Hh = self.cfg, self.C, ctx.T, self.Hh
+        rx = x if resid is None else resid
         H, ql, lat, rope, nope, vd = cfg.hidden, cfg.q_lora_rank, cfg.kv_lora_rank, cfg.qk_rope_dim, cfg.qk_nope_dim, cfg.v_head_dim
         hq, hs = self._fp8("h", T, H)
         qkva = self.ws.get("qkva", (T, ql + lat + rope), torch.bfloat16)
@@ -625,9 +642,9 @@ class NativeRunner:
             C.mla_prefill(qf, kvb.view(T, Hh, nope + vd), kr, ctx.cu_seqlens, ctx.max_len, self.scale,
                           ovq, ovs, None)
         if getattr(lw, "attn_tp", True):
-            self._row_parallel_out(ovq, ovs, lw.o, x, out, T)
+            self._row_parallel_out(ovq, ovs, lw.o, rx, out, T)
         else:       # replicated attention: the whole o projection, residual added, no reduction
-            self._gemv(ovq, ovs, lw.o, out, x)
+            self._gemv(ovq, ovs, lw.o, out, rx)
 
     def _indexer(self, lw, hq, hs, qaq, qas, ctx, li):
         """DSA indexer: insert this step's keys, score every cached position
@@ -655,8 +672,10 @@ class NativeRunner:
         C.indexer_topk(scores, cfg.index_topk, sel)
         return sel
 
-    def _ffn(self, lw: LayerWeights, x, ctx: StepCtx, out):
+    def _ffn(self, lw: LayerWeights, x, ctx: StepCtx, out, resid=None):
+        """out = resid + ffn(norm(x)); resid defaults to x."""
         cfg, C, T = self.cfg, self.C, ctx.T
+        rx = x if resid is None else resid
         H = cfg.hidden
         hb = self.ws.get("hb", (T, H), torch.bfloat16)
         hq, hs = self._fp8("h", T, H)
@@ -667,7 +686,7 @@ class NativeRunner:
             self._gemv(hq, hs, lw.gate_up, gu)
             aq, as_ = self._fp8("act", T, I2 // 2)
             C.swiglu_quant(gu, 0.0, None, 0, aq, as_)
-            self._row_parallel_out(aq, as_, lw.down, x, out, T)
+            self._row_parallel_out(aq, as_, lw.down, rx, out, T)
             return
         h2q, h2s = self._fp8("h2", T, H)
         self._norm_in(x, lw.ffn_norm, hb, hq, hs, h2q, h2s)
@@ -716,9 +735,9 @@ class NativeRunner:
                 self._join()
             none = self.ws.get("ep.nopos", (0,), torch.int32)
             if fused:
-                C.moe_combine(self.ep.ret[:R], none, wts, x, sh, out, None, None, self.ep.desc)
+                C.moe_combine(self.ep.ret[:R], none, wts, rx, sh, out, None, None, self.ep.desc)
             else:
-                C.moe_combine(yk, none, wts, x, sh, out, None)
+                C.moe_combine(yk, none, wts, rx, sh, out, None)
             return
         if T <= 64 and not use_tc and H % 1024 == 0 and topp <= 0:
             # decode: logits + top-k + pair list in one launch
@@ -756,18 +775,18 @@ class NativeRunner:
         if sh is not None:
             self._join()
         if self.tp_group is None:
-            C.moe_combine(y2, posof, wts, x, sh, out, None)
+            C.moe_combine(y2, posof, wts, rx, sh, out, None)
         elif self._fused:
             C.moe_combine(y2, posof, wts, None, sh, None, None, self.ar.desc)
-            self._pend = (x, out)
+            self._pend = (rx, out)
         else:
             part = self.ws.get("moe_part", (T, H), torch.bfloat16)
             C.moe_combine(y2, posof, wts, None, sh, part, None)
             self._tp_allreduce(part)
             if self._decode:
-                self._pend_add = (x, part, out)
+                self._pend_add = (rx, part, out)
             else:
-                torch.add(x, part, out=out)
+                torch.add(rx, part, out=out)
 
     def _moe_tc(self, h2q, h2s, ids, ex, R, T, E=None, e_lo=-1, MB=128):
         """Prefill experts on tensor cores: 128-row expert-aligned pairs, activations
@@ -876,6 +895,85 @@ class NativeRunner:
                 rows = bad.view(t.shape[0], -1).any(-1).nonzero().flatten()[:8].tolist()
                 raise FloatingPointError(f"non-finite values after {name}: shape {tuple(t.shape)}, rows {rows}")
 
+    # ------------------------------------------------------------------ hyper-connections
+    def _init_hyper_connections(self):
+        """hc_mult > 1 (DeepSeek-V4 mHC): the residual is n f32 streams per token; every
+        site's mixing weights as f32 device tensors, and the MTP module's eh_proj split into
+        its embedding and hidden halves (the hidden half projects each stream)."""
+        self.hcn = self.cfg.hc_mult
+        self._hc = {}
+        self._hc_pend = None      # (block output, post, comb) the next site's hc_mix applies
+        if self.hcn <= 1:
+            return
+        H = self.cfg.hidden
+        if H % 128:
+            raise NotImplementedError("hyper-connections on the GPU: hidden % 128")
+        sites = []
+        for lw in self.mw.layers:
+            sites += [lw.hc_attn, lw.hc_ffn]
+        if self.mw.extra.get("hc_head") is not None:
+            sites.append(self.mw.extra["hc_head"])
+        m = self.mw.mtp
+        if m is not None:
+            sites += [m.layer.hc_attn, m.layer.hc_ffn, m.hc_head]
+            self._eh_e, self._eh_h = (_split_cols(m.eh_proj, 0, H), _split_cols(m.eh_proj, H, 2 * H))
+        for hc in sites:
+            if hc is None:
+                raise ValueError("hyper-connections: a site without mixing weights")
+            self._hc[id(hc)] = tuple(t.to(self.dev, torch.float32).contiguous() for t in (hc.fn, hc.base, hc.scale))
+
+    def _hc_site(self, xs, hc, T):
+        """One site: the pending block update (if any) and the partial mixes in one kernel,
+        then the mixes and the block input h (bf16 [T, H])."""
+        n, H, cfg = self.hcn, self.cfg.hidden, self.cfg
+        fn, base, scale = self._hc[id(hc)]
+        R = fn.shape[0]
+        part = self.ws.get("hc.part", (H // 128, T, R + 1), torch.float32)
+        h = self.ws.get("hc.h", (T, H), torch.bfloat16)
+        post = self.ws.get("hc.post", (T, n), torch.float32)
+        comb = self.ws.get("hc.comb", (T, n, n), torch.float32)
+        upd, self._hc_pend = self._hc_pend, None
+        if upd is not None:
+            self.C.hc_mix(xs, upd[0], upd[1], upd[2], fn, part)
+        else:
+            self.C.hc_mix(xs, None, None, None, fn, part)
+        block = R != n
+        self.C.hc_apply(xs, part, base, scale, cfg.hc_eps, cfg.hc_sinkhorn_iters, cfg.rms_eps, h,
+                        post if block else None, comb if block else None)
+        return h
+
+    def _hc_flush(self, xs):
+        """Apply the last block's pending update to the streams."""
+        upd, self._hc_pend = self._hc_pend, None
+        if upd is not None:
+            self.C.hc_mix(xs, upd[0], upd[1], upd[2])
+
+    def _layer_hc(self, lw, xs, ctx, cache, li):
+        """A decoder layer over the streams xs [T, n, H] (updated in place): each block reads
+        its site's h and adds nothing itself (zero residual); the streams take its output
+        through the next site's hc_mix."""
+        T, H = ctx.T, self.cfg.hidden
+        self._fused = False       # no deferred residual adds: every block output is complete
+        self._decode = False
+        zero = self.ws.get("hc.zero", (T, H), torch.bfloat16)
+        zero.zero_()
+        timed = self.timers is not None and ctx.mode in ("prefill", "cached")
+        h = self._hc_site(xs, lw.hc_attn, T)
+        a = self.ws.get("x_mid", (T, H), torch.bfloat16)
+        with self.timers.span("prefill.attention") if timed else contextlib.nullcontext():
+            self._attention(lw, h, ctx, cache, li, a, resid=zero)
+        self._check(f"attention[{li}] ({ctx.mode})", a)
+        self._hc_pend = (a, self.ws.get("hc.post", (T, self.hcn), torch.float32),
+                         self.ws.get("hc.comb", (T, self.hcn, self.hcn), torch.float32))
+        h = self._hc_site(xs, lw.hc_ffn, T)
+        f = self.ws.get("hc.f", (T, H), torch.bfloat16)
+        with (self.timers.span("prefill.moe" if self.cfg.is_moe_layer(li) else "prefill.dense_ffn") if timed
+              else contextlib.nullcontext()):
+            self._ffn(lw, h, ctx, f, resid=zero)
+        self._check(f"ffn[{li}] ({ctx.mode})", f)
+        self._hc_pend = (f, self.ws.get("hc.post", (T, self.hcn), torch.float32),
+                         self.ws.get("hc.comb", (T, self.hcn, self.hcn), torch.float32))
+
     def _layer(self, lw, x, ctx, cache, li):
         H = self.cfg.hidden
         self._fused = (self.ar is not None and ctx.mode == "decode" and ctx.T <= self.fused_max_t
@@ -901,6 +999,15 @@ class NativeRunner:
         else:       # activations of the previous pipeline stage
             torch.distributed.recv(xin, src=self._pp_peer(self.pp_rank - 1), group=self.pp_group)
         x = xin
+        if self.hcn > 1:          # n residual streams, each starting as the embedding
+            if not (self.first_stage and self.last_stage):
+                raise NotImplementedError("hyper-connections: no pipeline stages on the GPU")
+            x = self.ws.get("hc.x", (ctx.T, self.hcn, self.cfg.hidden), torch.float32)
+            x.copy_(xin[:, None, :].expand(-1, self.hcn, -1))
+            for li, lw in enumerate(self.mw.layers):
+                self._layer_hc(lw, x, ctx, self.kv[li], li)
+            self._hc_flush(x)
+            return x
         for li, lw in enumerate(self.mw.layers):
             x = self._layer(lw, x, ctx, self.kv[li], li)
         if not self.last_stage:
@@ -912,12 +1019,18 @@ class NativeRunner:
         """final RMSNorm -> (normed hidden bf16 [T,H], logits f32 [T,V])."""
         cfg, C = self.cfg, self.C
         T = x.shape[0]
+        streams = None
+        if self.hcn > 1:          # x: the streams [T, n, H]; the head's gated sum feeds the norm
+            streams = x
+            x = self._hc_site(x, self.mw.extra["hc_head"] if tag == "main" else self.mw.mtp.hc_head, T)
         hid = self.ws.get(tag + ".hid", (T, cfg.hidden), torch.bfloat16)
         fq, fs = self._fp8(tag + ".f", T, cfg.hidden)
         self._norm_in(x, self.mw.final_norm if tag == "main" else self.mw.mtp.head_norm, hid, fq, fs)
         logits = self.ws.get(tag + ".logits", (T, self.mw.lm_head.w.shape[0]), torch.float32)
         self._gemv(fq, fs, self.mw.lm_head, logits)
         self._check(f"lm_head ({tag})", logits)
+        if streams is not None:   # the MTP module reads the pre-head streams [T, n H]
+            return streams.reshape(T, -1), logits
         return hid, logits
 
     def _mtp(self, hidden, next_tokens, ctx: StepCtx, rows=None):
@@ -926,6 +1039,8 @@ class NativeRunner:
         T, H = ctx.T, cfg.hidden
         table = self.mw.embed if self.mw.embed is not None else self.mw.extra["mtp_embed"]
         emb = torch.nn.functional.embedding(next_tokens.long(), table)
+        if self.hcn > 1:
+            return self._mtp_hc(hidden, emb, ctx, rows)
         ehq, ehs = self._fp8("eh", T, 2 * H)
         C.rmsnorm_quant(emb, None, None, m.enorm, cfg.rms_eps, None, ehq, ehs, None, None, 2 * H)
         C.rmsnorm_quant(hidden, None, None, m.hnorm, cfg.rms_eps, None, ehq[:, H:], ehs[:, H // 64:], None, None,
@@ -937,6 +1052,32 @@ class NativeRunner:
         if rows is not None:      # only these rows need the head (e.g. the last row of each prompt)
             x = x[rows].contiguous()
         return self._final(x, None, "mtp")
+
+    def _mtp_hc(self, hidden, emb, ctx, rows):
+        """The MTP module over streams: hidden [T, n H] (pre-head streams), each stream normed
+        and projected by eh_proj's hidden half, plus the normed next-token embedding (zero at
+        position 0) through its embedding half; the MTP layer over the streams, the module's
+        stream reduction and head norm, the shared head."""
+        cfg, C, m, n = self.cfg, self.C, self.mw.mtp, self.hcn
+        T, H = ctx.T, cfg.hidden
+        emb = emb * (ctx.pos != 0).to(emb.dtype)[:, None]
+        eq, es = self._fp8("mhc.e", T, H)
+        C.rmsnorm_quant(emb.contiguous(), None, None, m.enorm, cfg.rms_eps, None, eq, es, None, None, 0)
+        hb = hidden.reshape(T * n, H).to(torch.bfloat16)
+        hq, hs = self._fp8("mhc.h", T * n, H)
+        C.rmsnorm_quant(hb, None, None, m.hnorm, cfg.rms_eps, None, hq, hs, None, None, 0)
+        ye = self.ws.get("mhc.ye", (T, H), torch.float32)
+        self._gemv(eq, es, self._eh_e, ye)
+        yh = self.ws.get("mhc.yh", (T * n, H), torch.float32)
+        self._gemv(hq, hs, self._eh_h, yh)
+        xs = self.ws.get("hc.xm", (T, n, H), torch.float32)
+        torch.add(yh.view(T, n, H), ye[:, None, :], out=xs)
+        self._check("mtp eh_proj", xs)
+        self._layer_hc(m.layer, xs, ctx, self.kv[-1], len(self.mw.layers))
+        self._hc_flush(xs)
+        if rows is not None:
+            xs = xs[rows].contiguous()
+        return self._final(xs, None, "mtp")
 
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
@@ -961,9 +1102,12 @@ class NativeRunner:
             self._key_rows(ctx, [end])
         x = self._main(toks, ctx)
         if self.last_stage and self.k:
-            hid_all = self.ws.get("pf.hid", (T, self.cfg.hidden), torch.bfloat16)
-            self.C.rmsnorm_quant(x, None, None, self.mw.final_norm, self.cfg.rms_eps, hid_all, None, None, None,
-                                 None, 0)
+            if self.hcn > 1:       # the MTP module reads the streams
+                hid_all = x.reshape(T, -1)
+            else:
+                hid_all = self.ws.get("pf.hid", (T, self.cfg.hidden), torch.bfloat16)
+                self.C.rmsnorm_quant(x, None, None, self.mw.final_norm, self.cfg.rms_eps, hid_all, None, None,
+                                     None, None, 0)
             nxt = torch.tensor(prompt[start + 1:end + 1], dtype=torch.int32, device=dev)
             self._mtp(hid_all, nxt, ctx, rows=torch.tensor([T - 1], device=dev))
         self.check_status("prefill chunk")
@@ -1047,8 +1191,11 @@ class NativeRunner:
             self._pp_broadcast_state(state)
             return tgt
         # full hidden for the MTP pass: final norm over all rows
-        hid_all = self.ws.get("pf.hid", (T, self.cfg.hidden), torch.bfloat16)
-        C.rmsnorm_quant(x, None, None, self.mw.final_norm, self.cfg.rms_eps, hid_all, None, None, None, None, 0)
+        if self.hcn > 1:           # the MTP module reads the streams
+            hid_all = x.reshape(T, -1)
+        else:
+            hid_all = self.ws.get("pf.hid", (T, self.cfg.hidden), torch.bfloat16)
+            C.rmsnorm_quant(x, None, None, self.mw.final_norm, self.cfg.rms_eps, hid_all, None, None, None, None, 0)
         nxt = torch.empty_like(toks)
         nxt[:-1] = toks[1:]
         nxt[last] = tgt

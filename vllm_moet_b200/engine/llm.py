@@ -96,9 +96,9 @@ class LLM:
             speculative_method = "dspark"
         if speculative_method == "dspark" and self.device.type == "cuda":
             raise NotImplementedError("DSpark / DFlash block drafting runs on the CPU engine; the GPU runner drafts with MTP")
-        if cfg.hc_mult > 1 and self.device.type == "cuda":
-            raise NotImplementedError("hyper-connections (hc_mult > 1) run on the CPU engine; the GPU layer kernels "
-                                      "keep one residual stream")
+        if cfg.hc_mult > 1 and self.device.type == "cuda" and pipeline_parallel_size > 1:
+            raise NotImplementedError("hyper-connections on the GPU: no pipeline stages (the stage boundary "
+                                      "carries one residual stream)")
         simple_dspark = speculative_method == "dspark" and ((dspark or {}).get("model", "context") != "context"
                                                             or (dspark or {}).get("drafter") is not None)
         if cfg.hc_mult > 1 and (sp_group is not None or simple_dspark):
