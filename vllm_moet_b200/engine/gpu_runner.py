@@ -47,6 +47,26 @@ def _split_cols(lin, k0: int, k1: int):
     raise NotImplementedError(f"column split of {type(lin).__name__}")
 
 
+def dcp_local_count(n, W: int, r: int, I: int):
+    """How many of positions [0, n) rank r of W holds when position p lives on rank
+    (p // I) % W (ints or tensors)."""
+    cyc = I * W
+    rem = n % cyc - r * I
+    if isinstance(rem, torch.Tensor):
+        return (n // cyc) * I + rem.clamp(0, I)
+    return (n // cyc) * I + min(max(rem, 0), I)
+
+
+def dcp_slots(bt, seq, pos, W: int, r: int, I: int):
+    """Cache slots of positions `pos` of rows `seq` on rank r: the rank keeps its positions
+    densely (local index (p // (I W)) I + p % I through its block table); -1 where another
+    rank holds the position."""
+    own = (pos // I) % W == r
+    lp = (pos // (I * W)) * I + pos % I
+    blk = bt[seq, torch.where(own, lp // KV_BLOCK, torch.zeros_like(lp))].long()
+    return torch.where(own, blk * KV_BLOCK + lp % KV_BLOCK, torch.full_like(lp, -1))
+
+
 class Workspace:
     """Grow-only named device buffers; frozen once a graph has been captured."""
 
@@ -93,6 +113,9 @@ class StepCtx:
     # [0, end_i)) and their cu_seqlens; None = attention reads the paged cache (absorbed)
     kv_idx: Optional[torch.Tensor] = None
     cu_k: Optional[torch.Tensor] = None
+    # decode context parallelism: per row, the index of its last key among this rank's
+    # positions (-1: none yet); None without DCP
+    lpos: Optional[torch.Tensor] = None
 
 
 class NativeRunner:
@@ -137,6 +160,7 @@ class NativeRunner:
         self.ep = None            # expert-parallel all-to-all buffers (EpSymm) under DP attention + EP
         self.ep_group = None
         self.sp_group = None      # sequence-parallel prefill ranks (replicated weights)
+        self.dcp = None           # decode context parallelism: (group, world, rank, interleave)
         self._sp = None           # active SP prefill: (group, world, rank, block ids per rank's chunk)
         self.cache = None         # residency.ExpertCache when routed experts are served from a host store
         self.delta = None         # residency.DeltaTier (FP4 hot experts) when enabled
@@ -357,6 +381,35 @@ class NativeRunner:
         position.  Afterwards every rank holds the prompt's full caches and decodes it
         (replicated, deterministic)."""
         self.sp_group = group
+
+    def set_dcp_group(self, group, interleave: int = 1):
+        """Decode context parallelism over `group` (replicated weights): position p's latent
+        cache row lives only on rank (p // interleave) % W.  Prefill computes every row on
+        every rank and writes the owned ones; a decode-sized attention runs the split-KV
+        kernel over the rank's own rows, all-gathers the (partial output, max, sum) splits of
+        every rank and merges them in one fixed order (so every rank emits the same tokens)."""
+        import torch.distributed as dist
+        if self.cfg.index_heads:
+            raise NotImplementedError("GPU DCP: dense MLA attention only (no DSA indexer)")
+        W = dist.get_world_size(group)
+        if W > 32:
+            raise ValueError("GPU DCP: at most 32 ranks (one merge warp)")
+        self.dcp = (group, W, dist.get_rank(group), int(interleave))
+
+    def _slots(self, bt, seq, pos):
+        """Cache slots of (row, position) pairs (DCP: this rank's, -1 elsewhere)."""
+        seq, pos = seq.long(), pos.long()
+        if self.dcp is None:
+            return bt[seq, pos // KV_BLOCK].long() * KV_BLOCK + pos % KV_BLOCK
+        _, W, r, I = self.dcp
+        return dcp_slots(bt, seq, pos, W, r, I)
+
+    def _lpos(self, pos):
+        """DCP: per row, the local index of the last key it sees (None without DCP)."""
+        if self.dcp is None:
+            return None
+        _, W, r, I = self.dcp
+        return (dcp_local_count(pos.long() + 1, W, r, I) - 1).int()
 
     def sp_chunk(self, n: int):
         """-> (chunk length, block-aligned) of an n-token prompt over the SP group, or None
@@ -606,9 +659,19 @@ class NativeRunner:
             if ctx.mode != "decode":
                 self._sp_gather(self.kv, li)  # SP prefill: the other ranks' chunks of this layer's cache
             S = max(1, min(32, 256 // T))
+            if ctx.lpos is not None:
+                S = max(1, min(S, 32 // self.dcp[1]))
             opart = self.ws.get("opart", (S, T, Hh, lat), torch.float32)
             mlp = self.ws.get("mlpart", (S, T, Hh, 2), torch.float32)
-            C.mla_decode(qcat, cache, ctx.block_table, ctx.seq, ctx.pos, opart, mlp, self.scale, self.status, sel)
+            C.mla_decode(qcat, cache, ctx.block_table, ctx.seq, ctx.pos if ctx.lpos is None else ctx.lpos, opart,
+                         mlp, self.scale, self.status, sel)
+            if ctx.lpos is not None:      # DCP: every rank's splits, merged below in rank order
+                G, W = self.dcp[0], self.dcp[1]
+                oall = self.ws.get("dcp.opart", (W * S, T, Hh, lat), torch.float32)
+                mall = self.ws.get("dcp.mlpart", (W * S, T, Hh, 2), torch.float32)
+                torch.distributed.all_gather_into_tensor(oall, opart, group=G)
+                torch.distributed.all_gather_into_tensor(mall, mlp, group=G)
+                opart, mlp = oall, mall
             # split merge + W_uv + e4m3 quantisation in one kernel
             C.mla_combine_uv(opart, mlp, lw.w_uv.w, lw.w_uv.s, ovq, ovs)
         elif flash_cached:
@@ -1164,7 +1227,7 @@ class NativeRunner:
         pos = torch.cat([torch.arange(s0, n, dtype=torch.int32) for s0, n in zip(starts, full)]).to(dev)
         seq = torch.cat([torch.full((n,), i, dtype=torch.int32) for i, n in enumerate(lens)]).to(dev)
         bt = torch.tensor(block_tables, dtype=torch.int32, device=dev)
-        slot = (bt[seq.long(), (pos // KV_BLOCK).long()].long() * KV_BLOCK + (pos % KV_BLOCK).long())
+        slot = self._slots(bt, seq, pos)
         cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=dev)
         ctx = StepCtx(T=T, pos=pos, seq=seq, slot=slot, block_table=bt,
                       mode="cached" if any(starts) else "prefill", cu_seqlens=cu, max_len=max(lens), mb=32)
@@ -1210,8 +1273,8 @@ class NativeRunner:
         for j in range(1, self.k):
             p2 = cur_pos + (j - 1)
             s2 = torch.arange(B, dtype=torch.int32, device=dev)
-            slot2 = bt[s2.long(), (p2 // KV_BLOCK).long()].long() * KV_BLOCK + (p2 % KV_BLOCK).long()
-            ctx2 = StepCtx(T=B, pos=p2, seq=s2, slot=slot2, block_table=bt, mode="decode", mb=8)
+            slot2 = self._slots(bt, s2, p2)
+            ctx2 = StepCtx(T=B, pos=p2, seq=s2, slot=slot2, block_table=bt, mode="decode", mb=8, lpos=self._lpos(p2))
             h_prev, lg = self._mtp(h_prev.clone(), prev_tok, ctx2)
             dj = self.ws.get("pf.dj", (B,), torch.int32)
             self._argmax(lg, dj)
@@ -1259,11 +1322,10 @@ class NativeRunner:
             self.miss.zero_()
         B = st.B
         pos = st.seq_pos
-        blk = st.block_table.gather(1, (pos // KV_BLOCK).long().view(B, 1)).view(-1)
-        slot = blk.long() * KV_BLOCK + (pos % KV_BLOCK).long()
+        slot = self._slots(st.block_table, st.arange_b, pos)
         slot = torch.where(st.active.bool(), slot, torch.full_like(slot, -1))
         ctx = StepCtx(T=B, pos=pos.int(), seq=st.arange_b, slot=slot, block_table=st.block_table, mode="decode",
-                      mb=8)
+                      mb=8, lpos=self._lpos(pos))
         x = self._main(st.tokens[:, 0].contiguous(), ctx)
         _, logits = self._final(x, None, "main")
         am = self.ws.get("dec.am", (B,), torch.int32)
@@ -1329,11 +1391,10 @@ class NativeRunner:
         kp1 = k + 1
         T = B * kp1
         pos = (st.seq_pos[:, None] + st.arange_kp1[None, :]).reshape(-1)
-        blk = st.block_table.gather(1, (pos // KV_BLOCK).long().view(B, kp1)).reshape(-1)
-        slot = blk.long() * KV_BLOCK + (pos % KV_BLOCK).long()
+        slot = self._slots(st.block_table, st.seq_rows, pos)
         slot = torch.where(st.active_rows, slot, torch.full_like(slot, -1))
         ctx = StepCtx(T=T, pos=pos.int(), seq=st.seq_rows, slot=slot, block_table=st.block_table, mode="decode",
-                      mb=8 if T * self.cfg.top_k <= self.mb8_max_r else 16)
+                      mb=8 if T * self.cfg.top_k <= self.mb8_max_r else 16, lpos=self._lpos(pos))
         x = self._main(st.tokens.view(-1), ctx)
         if not self.last_stage:
             self._pp_broadcast_state(st)
@@ -1360,11 +1421,10 @@ class NativeRunner:
         for j in range(1, k):
             self._route_tag = f".p{j}"
             p2 = st.seq_pos + st.n_acc + j
-            blk2 = st.block_table.gather(1, (p2 // KV_BLOCK).long().view(B, 1)).view(-1)
-            slot2 = blk2.long() * KV_BLOCK + (p2 % KV_BLOCK).long()
+            slot2 = self._slots(st.block_table, st.arange_b, p2)
             slot2 = torch.where(st.active.bool(), slot2, torch.full_like(slot2, -1))
             ctx2 = StepCtx(T=B, pos=p2.int(), seq=st.arange_b, slot=slot2, block_table=st.block_table,
-                           mode="decode", mb=8)
+                           mode="decode", mb=8, lpos=self._lpos(p2))
             h_prev, lg = self._mtp(h_prev, prev_tok, ctx2)
             dj = self.ws.get("dec.dj", (B,), torch.int32)
             self._argmax(lg, dj)

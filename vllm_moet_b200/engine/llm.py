@@ -78,8 +78,11 @@ class LLM:
             device = "cuda" if torch.cuda.is_available() else "cpu"
         self.device = torch.device(device)
         self._tp_group, self._pp_group = tp_group, pp_group
-        if self.device.type == "cuda" and dcp_group is not None:
-            raise NotImplementedError("DCP decode runs on the CPU engine")
+        # ranks that must draw the same sampling seeds (they emit the same tokens)
+        self._seed_group = tp_group if tp_group is not None else dcp_group
+        if self.device.type == "cuda" and dcp_group is not None and cfg.index_heads:
+            raise NotImplementedError("GPU DCP decode: dense MLA attention (DSA models run DCP on the CPU engine)")
+        self._dcp = None
         if self.device.type == "cuda" and sp_group is not None and (enable_prefix_caching or enable_chunked_prefill):
             raise NotImplementedError("GPU SP prefill: no prefix caching or chunked prefill")
         self._sp_group = sp_group
@@ -204,6 +207,10 @@ class LLM:
             self.runner = NativeRunner(self.mw, self.ecfg, nb, self.device)
             if sp_group is not None:
                 self.runner.set_sp_group(sp_group)
+            if dcp_group is not None:
+                import torch.distributed as dist
+                self.runner.set_dcp_group(dcp_group, dcp_interleave)
+                self._dcp = (dist.get_world_size(dcp_group), dist.get_rank(dcp_group), int(dcp_interleave))
             if ep_group is not None:
                 # the most routed rows of one decode-sized layer on one rank: verify rows x top-k
                 self.runner.set_ep_group(ep_group, self._bucket(max_num_seqs) * (self.k + 1) * cfg.top_k)
@@ -727,11 +734,12 @@ class LLM:
             pc = getattr(self.blocks, "prefix_caching", False)
             starts = []
             while waiting and free and self.blocks.can_allocate(
-                    len(waiting[0].prompt) + waiting[0].params.max_tokens + kp1 + 1, waiting[0].prompt if pc else None):
+                    self._kv_rows(len(waiting[0].prompt) + waiting[0].params.max_tokens + kp1 + 1),
+                    waiting[0].prompt if pc else None):
                 r = waiting.popleft()
                 r.row = free.pop(0)
                 rows[r.row] = r
-                n_tok = len(r.prompt) + r.params.max_tokens + kp1 + 1
+                n_tok = self._kv_rows(len(r.prompt) + r.params.max_tokens + kp1 + 1)
                 if pc:
                     # shared prefix blocks; the block holding the position before the first new
                     # token is copied and that position computed again (its MTP entry differs)
@@ -1022,10 +1030,17 @@ class LLM:
                         [p.seed if p.seed is not None else d for p, d in zip(ps, drawn)])
         return True
 
+    def _kv_rows(self, n: int) -> int:
+        """Cache rows this rank keeps for n positions (DCP: only its own positions)."""
+        if getattr(self, "_dcp", None) is None:
+            return n
+        from .gpu_runner import dcp_local_count
+        return dcp_local_count(n, *self._dcp)
+
     def _shared_seeds(self, n: int) -> list:
         """n random seeds, equal on every rank of the tensor-parallel group."""
         from .sampling_params import shared_seeds
-        return shared_seeds(n, self._tp_group, self.device)
+        return shared_seeds(n, self._seed_group, self.device)
 
     def _delta_step(self, st, B, graph, kp1):
         """After a decode step: feed routing to the delta tier's frequency policy and,
