@@ -21,6 +21,14 @@ class Stub:
         self.ws_prefill = self.ws
         self.cached_flash_min = 1
         self.hcn = 1
+        self.dcp = None
+        self.eagle = None
+
+    def _slots(self, bt, seq, pos):
+        return NativeRunner._slots(self, bt, seq, pos)
+
+    def _lpos(self, pos):
+        return None
 
     def _key_rows(self, ctx, ends):
         return NativeRunner._key_rows(self, ctx, ends)

@@ -261,5 +261,7 @@ def test_eagle3_drafts_from_aux_hidden_states():
     prompts = [[5, 6, 7, 8, 9, 10, 11], [5, 6, 7, 8, 20]]
     out = [o.outputs[0].token_ids for o in llm.generate(prompts, SamplingParams(max_tokens=10, ignore_eos=True))]
     assert out == [reference.greedy_generate(llm.mw, p, 10) for p in prompts]
+    with pytest.raises(NotImplementedError):       # the GPU runner drafts EAGLE-3 on one GPU per replica
+        LLM("tiny-moe", device="cuda", speculative_method="eagle3", tensor_parallel_size=2)
     with pytest.raises(NotImplementedError):
-        LLM("tiny-moe", device="cuda", speculative_method="eagle3")
+        LLM("tiny-moe", device="cuda", speculative_method="eagle3", hc_mult=4)

@@ -125,7 +125,8 @@ class NativeRunner:
         self.cfg: ModelConfig = mw.cfg
         self.ecfg = ecfg
         self.dev = torch.device(device)
-        has_mtp = mw.mtp is not None or (mw.extra.get("pp_size", 1) > 1 and mw.cfg.num_mtp_layers > 0)
+        self._init_draft_module(mw)
+        has_mtp = self._draft is not None or (mw.extra.get("pp_size", 1) > 1 and mw.cfg.num_mtp_layers > 0)
         self.k = ecfg.num_speculative_tokens if has_mtp else 0
         # heads per rank: all of them when attention is replicated across the TP group
         attn_tp = all(getattr(lw, "attn_tp", True) for lw in mw.layers)
@@ -133,7 +134,7 @@ class NativeRunner:
         cfg = self.cfg
         self.num_blocks = num_blocks
         self.kv_mode = 2 if ecfg.kv_cache_dtype == "nvfp4" else 1
-        n_cache = len(mw.layers) + (1 if mw.mtp is not None else 0)
+        n_cache = len(mw.layers) + (1 if self._draft is not None else 0)
         if self.kv_mode == 2:      # NVFP4 latent cache: 352 bytes per token (3.3x the context of bf16 rows)
             self.kv = [torch.zeros(num_blocks, KV_BLOCK, NVFP4_ROW, dtype=torch.uint8, device=self.dev)
                        for _ in range(n_cache)]
@@ -144,7 +145,7 @@ class NativeRunner:
         # DSA indexer key caches (bf16 [blocks, 64, D] per layer with an indexer)
         self.idx_kv = [torch.zeros(num_blocks, KV_BLOCK, cfg.index_head_dim, dtype=torch.bfloat16, device=self.dev)
                        if lw.idx_wq is not None else None
-                       for lw in list(mw.layers) + ([mw.mtp.layer] if mw.mtp is not None else [])]
+                       for lw in list(mw.layers) + ([self._draft.layer] if self._draft is not None else [])]
         self.status = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.miss = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.ws_decode_by_bucket = {}
@@ -958,6 +959,36 @@ class NativeRunner:
                 rows = bad.view(t.shape[0], -1).any(-1).nonzero().flatten()[:8].tolist()
                 raise FloatingPointError(f"non-finite values after {name}: shape {tuple(t.shape)}, rows {rows}")
 
+    # ------------------------------------------------------------------ draft module
+    def _init_draft_module(self, mw):
+        """The module the decode step drafts with: the MTP module, or an EAGLE-3 module
+        (``mw.extra["eagle3"]``) seen through the same fields -- its input projection plays
+        eh_proj, its norm the head norm -- plus ``fc`` over the target's aux hidden states
+        (the residual after each target layer, concatenated).  FP8 copies of its BF16
+        projections serve the FP8 GEMV / GEMM kernels."""
+        import types
+        from ..models.weights import Fp8Linear
+        self.eagle = mw.extra.get("eagle3")
+        if self.eagle is None:
+            self._draft = mw.mtp
+            return
+        ew = self.eagle
+
+        def fp8(lin):
+            return lin if isinstance(lin, Fp8Linear) else Fp8Linear.from_float(lin.dequant().to(self.dev))
+        self._eagle_fc = fp8(ew.fc)
+        self._eagle_layers = {li: j for j, li in enumerate(ew.target_layers)}
+        self._draft = types.SimpleNamespace(enorm=ew.enorm, hnorm=ew.hnorm, eh_proj=fp8(ew.in_proj), layer=ew.layer,
+                                            head_norm=ew.norm, hc_head=None)
+
+    def _eagle_aux(self, T):
+        """The target's aux hidden states [T, n H] of the last main pass (EAGLE-3)."""
+        return self.ws.get("eagle.aux", (T, len(self._eagle_layers) * self.cfg.hidden), torch.bfloat16)
+
+    def _draft_input(self, hid, T):
+        """What the first draft pass reads: the final normed hidden (MTP) or the aux states."""
+        return self._eagle_aux(T) if self.eagle is not None else hid
+
     # ------------------------------------------------------------------ hyper-connections
     def _init_hyper_connections(self):
         """hc_mult > 1 (DeepSeek-V4 mHC): the residual is n f32 streams per token; every
@@ -1073,6 +1104,9 @@ class NativeRunner:
             return x
         for li, lw in enumerate(self.mw.layers):
             x = self._layer(lw, x, ctx, self.kv[li], li)
+            if self.eagle is not None and li in self._eagle_layers:    # EAGLE-3 aux hidden state
+                H, j = self.cfg.hidden, self._eagle_layers[li]
+                self._eagle_aux(ctx.T)[:, j * H:(j + 1) * H].copy_(self._materialize(x))
         if not self.last_stage:
             x = self._materialize(x)
             torch.distributed.send(x.contiguous(), dst=self._pp_peer(self.pp_rank + 1), group=self.pp_group)
@@ -1088,7 +1122,7 @@ class NativeRunner:
             x = self._hc_site(x, self.mw.extra["hc_head"] if tag == "main" else self.mw.mtp.hc_head, T)
         hid = self.ws.get(tag + ".hid", (T, cfg.hidden), torch.bfloat16)
         fq, fs = self._fp8(tag + ".f", T, cfg.hidden)
-        self._norm_in(x, self.mw.final_norm if tag == "main" else self.mw.mtp.head_norm, hid, fq, fs)
+        self._norm_in(x, self.mw.final_norm if tag == "main" else self._draft.head_norm, hid, fq, fs)
         logits = self.ws.get(tag + ".logits", (T, self.mw.lm_head.w.shape[0]), torch.float32)
         self._gemv(fq, fs, self.mw.lm_head, logits)
         self._check(f"lm_head ({tag})", logits)
@@ -1098,12 +1132,18 @@ class NativeRunner:
 
     def _mtp(self, hidden, next_tokens, ctx: StepCtx, rows=None):
         """MTP module over rows (h_i, token_{i+1}) -> (head-normed hidden, logits)."""
-        cfg, C, m = self.cfg, self.C, self.mw.mtp
+        cfg, C, m = self.cfg, self.C, self._draft
         T, H = ctx.T, cfg.hidden
         table = self.mw.embed if self.mw.embed is not None else self.mw.extra["mtp_embed"]
         emb = torch.nn.functional.embedding(next_tokens.long(), table)
         if self.hcn > 1:
             return self._mtp_hc(hidden, emb, ctx, rows)
+        if self.eagle is not None and hidden.shape[-1] != H:     # EAGLE-3: aux states through fc
+            K = hidden.shape[-1]
+            aq, as_ = self._fp8("e3.aux", T, K)
+            C.quant_fp8(hidden, 0, aq, as_)
+            hidden = self.ws.get("e3.h", (T, H), torch.bfloat16)
+            self._gemv(aq, as_, self._eagle_fc, hidden)
         ehq, ehs = self._fp8("eh", T, 2 * H)
         C.rmsnorm_quant(emb, None, None, m.enorm, cfg.rms_eps, None, ehq, ehs, None, None, 2 * H)
         C.rmsnorm_quant(hidden, None, None, m.hnorm, cfg.rms_eps, None, ehq[:, H:], ehs[:, H // 64:], None, None,
@@ -1112,8 +1152,12 @@ class NativeRunner:
         self._gemv(ehq, ehs, m.eh_proj, xm)
         self._check("mtp eh_proj", xm)
         x = self._layer(m.layer, xm, ctx, self.kv[-1], len(self.mw.layers))
+        if self.eagle is not None:
+            x = self._materialize(x)
         if rows is not None:      # only these rows need the head (e.g. the last row of each prompt)
             x = x[rows].contiguous()
+        if self.eagle is not None:    # EAGLE-3 chains the draft layer's pre-norm output
+            return x, self._final(x, None, "mtp")[1]
         return self._final(x, None, "mtp")
 
     def _mtp_hc(self, hidden, emb, ctx, rows):
@@ -1167,6 +1211,8 @@ class NativeRunner:
         if self.last_stage and self.k:
             if self.hcn > 1:       # the MTP module reads the streams
                 hid_all = x.reshape(T, -1)
+            elif self.eagle is not None:
+                hid_all = self._eagle_aux(T)
             else:
                 hid_all = self.ws.get("pf.hid", (T, self.cfg.hidden), torch.bfloat16)
                 self.C.rmsnorm_quant(x, None, None, self.mw.final_norm, self.cfg.rms_eps, hid_all, None, None,
@@ -1256,6 +1302,8 @@ class NativeRunner:
         # full hidden for the MTP pass: final norm over all rows
         if self.hcn > 1:           # the MTP module reads the streams
             hid_all = x.reshape(T, -1)
+        elif self.eagle is not None:
+            hid_all = self._eagle_aux(T)
         else:
             hid_all = self.ws.get("pf.hid", (T, self.cfg.hidden), torch.bfloat16)
             C.rmsnorm_quant(x, None, None, self.mw.final_norm, self.cfg.rms_eps, hid_all, None, None, None, None, 0)
@@ -1411,7 +1459,7 @@ class NativeRunner:
             self._pp_broadcast_state(st)
             return
         # MTP pass 1 over the verify rows: (h_j, target_j) at position p + j
-        mh, mlog = self._mtp(hid, st.targets.view(-1), ctx)
+        mh, mlog = self._mtp(self._draft_input(hid, T), st.targets.view(-1), ctx)
         am = self.ws.get("dec.am", (T,), torch.int32)
         self._argmax(mlog, am)
         sel = (st.arange_b * kp1 + st.n_acc).long()

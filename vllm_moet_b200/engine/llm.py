@@ -89,9 +89,13 @@ class LLM:
         self._ep_group = ep_group
         if speculative_method not in ("mtp", "dspark", "dflash", "eagle3"):
             raise ValueError(f"speculative_method {speculative_method!r}: mtp | dspark | dflash | eagle3")
-        if speculative_method == "eagle3" and (self.device.type == "cuda" or pipeline_parallel_size > 1):
-            raise NotImplementedError("EAGLE-3 drafting runs on the CPU engine (one pipeline stage); the GPU runner "
-                                      "drafts with MTP")
+        if speculative_method == "eagle3" and pipeline_parallel_size > 1:
+            raise NotImplementedError("EAGLE-3 drafting runs on one pipeline stage")
+        if speculative_method == "eagle3" and self.device.type == "cuda" and (
+                tensor_parallel_size > 1 or tp_group is not None or ep_group is not None or sp_group is not None
+                or dcp_group is not None or cfg.hc_mult > 1):
+            raise NotImplementedError("GPU EAGLE-3 drafting: one GPU per replica (no TP / EP / SP / DCP), "
+                                      "single-stream models")
         if speculative_method == "dflash":
             # DFlash: the same parallel context drafter without the Markov and confidence
             # heads; every block is verified whole
@@ -1040,7 +1044,7 @@ class LLM:
     def _shared_seeds(self, n: int) -> list:
         """n random seeds, equal on every rank of the tensor-parallel group."""
         from .sampling_params import shared_seeds
-        return shared_seeds(n, self._seed_group, self.device)
+        return shared_seeds(n, getattr(self, "_seed_group", getattr(self, "_tp_group", None)), self.device)
 
     def _delta_step(self, st, B, graph, kp1):
         """After a decode step: feed routing to the delta tier's frequency policy and,

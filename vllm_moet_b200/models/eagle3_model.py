@@ -42,10 +42,10 @@ def random_eagle3_weights(mw: ModelWeights, target_layers: Optional[Sequence[int
     g = torch.Generator().manual_seed(seed + 3331)
     ones = torch.ones(H, dtype=torch.bfloat16, device=dev)
     layer = _make_layer(cfg, _Rng(seed + 3332, dev), 2000, dev, False)     # a dense draft layer
-    return Eagle3Weights(tl, make_linear(torch.randn(H, H * len(tl), generator=g) / math.sqrt(H * len(tl)), "bf16"),
-                         ones.clone(), ones.clone(),
-                         make_linear(torch.randn(H, 2 * H, generator=g) / math.sqrt(2 * H), "bf16"), layer,
-                         ones.clone())
+    fc = torch.randn(H, H * len(tl), generator=g) / math.sqrt(H * len(tl))
+    in_proj = torch.randn(H, 2 * H, generator=g) / math.sqrt(2 * H)
+    return Eagle3Weights(tl, make_linear(fc.to(dev), "bf16"), ones.clone(), ones.clone(),
+                         make_linear(in_proj.to(dev), "bf16"), layer, ones.clone())
 
 
 def attach_eagle3(mw: ModelWeights, ew: Eagle3Weights) -> ModelWeights:
