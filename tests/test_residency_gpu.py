@@ -192,3 +192,21 @@ def test_prefill_fp4(pf4, monkeypatch):
     else:
         assert e_base < e_fp4, (e_fp4, e_base)
     llm.shutdown()
+
+
+def test_router_lookahead_and_pilot_keep_tokens(resident_tokens, monkeypatch):
+    """LOOKA + PILOT over a small expert cache: the in-graph predictions and the host
+    prefetches never change the emitted tokens; the recall counters are rates, the
+    lookahead predictor scores every main-stack layer after the first."""
+    monkeypatch.setenv("VLLM_MOE_W2_FORCE_POOL", "1")
+    monkeypatch.setenv("VLLM_MOE_W2_LOOKA", "1")
+    monkeypatch.setenv("VLLM_MOE_W2_PILOT", "1")
+    monkeypatch.setenv("VLLM_MOE_W2_PILOT_K", "8")
+    llm = LLM(_cfg(), device="cuda", num_speculative_tokens=2, max_model_len=512, max_num_seqs=2,
+              expert_cache_slots=40, expert_store="pinned")
+    out = [o.outputs[0].token_ids for o in llm.generate(_prompts(), SamplingParams(max_tokens=12, ignore_eos=True))]
+    assert out == resident_tokens
+    r = llm.stats["looka_recall"]
+    assert r["routed"] > 0 and 0 <= r["previous_step"] <= 1 and 0 < r["router_lookahead"] <= 1
+    assert llm.stats["pilot"].get("requested", 0) + llm.stats["pilot"].get("warm_skips", 0) > 0
+    llm.shutdown()

@@ -240,6 +240,13 @@ class MoetConfig:
     spec_guard: float = 60.0            # replay-EMA percent that suppresses drafting (0 = off)
     spec_guard_ema: float = 0.02
     prefetch: bool = False              # prefetch the experts the next step's drafts routed to before
+    # router lookahead: layer L+1's router applied in-graph to layer L's MoE input predicts
+    # L+1's experts; LOOKA scores the predictions (recall counters), PILOT prefetches them
+    looka: bool = False
+    pilot: bool = False
+    pilot_k: int = 8                    # experts predicted per row
+    pilot_cap: int = 32                 # prefetches per step
+    pilot_min_replay: float = 30.0      # replay-EMA percent below which the pool counts as warm
     # bf12: lossless 12-bit container for dense BF16 linears, converted after load
     bf12: bool = False
     bf12_min_numel: int = 1 << 20
@@ -287,6 +294,11 @@ class MoetConfig:
         "spec_guard": "VLLM_MOE_W2_SPEC_GUARD",
         "spec_guard_ema": "VLLM_MOE_W2_SPEC_GUARD_EMA",
         "prefetch": "VLLM_MOE_W2_PREFETCH",
+        "looka": "VLLM_MOE_W2_LOOKA",
+        "pilot": "VLLM_MOE_W2_PILOT",
+        "pilot_k": "VLLM_MOE_W2_PILOT_K",
+        "pilot_cap": "VLLM_MOE_W2_PILOT_CAP",
+        "pilot_min_replay": "VLLM_MOE_W2_PILOT_MIN_REPLAY",
         "bf12": "VLLM_MOE_W2_BF12",
         "bf12_min_numel": "VLLM_MOE_W2_BF12_MIN_NUMEL",
         "bf12_verify": "VLLM_MOE_W2_BF12_VERIFY",
@@ -297,6 +309,8 @@ class MoetConfig:
         self.validate()
 
     def validate(self):
+        if not 1 <= int(self.pilot_k) <= 32:
+            raise ValueError("pilot_k (VLLM_MOE_W2_PILOT_K) must be in [1, 32]")
         if self.zero_mode not in ("auto", "sign", "alt"):
             raise ValueError(
                 f"VLLM_MOE_W2_ZERO_MODE must be one of auto|sign|alt, got {self.zero_mode!r}")

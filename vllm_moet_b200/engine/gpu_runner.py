@@ -166,6 +166,7 @@ class NativeRunner:
         self.cache = None         # residency.ExpertCache when routed experts are served from a host store
         self.delta = None         # residency.DeltaTier (FP4 hot experts) when enabled
         self._moe_index = {}
+        self._looka = None        # router lookahead (enable_looka)
         self._route_tag = ""      # routing-buffer suffix of the current MTP draft pass
         self._pend = None         # (residual, out) of a pushed reduction the next RMSNorm completes
         self._pend_add = None     # (residual, reduced partial, out): decode residual add left to the next norm
@@ -477,6 +478,61 @@ class NativeRunner:
         self.cache = cache
         self.miss = cache.miss_count
         self._moe_index = {id(lw): i for i, lw in enumerate(moe_layers(self.mw))}
+
+    def enable_looka(self, K: int, pilot: bool, max_rows: int):
+        """Router lookahead in the decode graph (expert cache attached): at every main-stack
+        MoE layer L, layer L + 1's router on L's MoE input predicts L + 1's top-K experts
+        (the model's own top-k selection with K picks).  Recall counters score them against
+        the routing L + 1 then does, and the previous step's routing of the same layer as
+        the baseline predictor; with ``pilot`` the predictions also go to ``pilot_log``
+        [layers, max_rows, K] for the host prefetcher.  (Reference: LOOKA / PILOT, patch
+        P:11740-11940.)"""
+        from ..residency import moe_layers
+        layers = moe_layers(self.mw)
+        n_main = sum(1 for lw in self.mw.layers if lw.is_moe)
+        k = self.cfg.top_k
+        self._looka = dict(K=int(K), layers=layers, n_main=n_main, rows=int(max_rows))
+        self.looka_hits = torch.zeros(2, dtype=torch.int64, device=self.dev)
+        self.looka_tot = torch.zeros(2, dtype=torch.int64, device=self.dev)
+        self._looka_prev = [torch.full((max_rows, k), -1, dtype=torch.int32, device=self.dev) for _ in range(n_main)]
+        self._looka_pred = torch.full((max_rows, int(K)), -1, dtype=torch.int32, device=self.dev)
+        self.pilot_log = (torch.full((n_main, max_rows, int(K)), -1, dtype=torch.int32, device=self.dev)
+                          if pilot else None)
+
+    def looka_recall(self) -> dict:
+        """Recall of the two predictors so far: the previous step's routing of the same
+        layer, and the router lookahead."""
+        h, t = self.looka_hits.tolist(), self.looka_tot.tolist()
+        return {"previous_step": h[0] / max(1, t[0]), "router_lookahead": h[1] / max(1, t[1]),
+                "routed": t[0]}
+
+    def _looka_step(self, mli, hb, ids, ctx):
+        """In-graph lookahead bookkeeping at main-stack MoE layer `mli` of a decode pass."""
+        L = self._looka
+        if L is None or mli is None or ctx.mode != "decode" or self._route_tag or mli >= L["n_main"]:
+            return
+        T, k = ids.shape
+        if T > L["rows"]:
+            return
+        prev = self._looka_prev[mli][:T]
+        self.looka_hits[0] += (ids.unsqueeze(2) == prev.unsqueeze(1)).any(dim=2).sum()
+        self.looka_tot[0] += T * k
+        prev.copy_(ids)
+        pred = self._looka_pred[:T]
+        if mli > 0:
+            self.looka_hits[1] += (ids.unsqueeze(2) == pred.unsqueeze(1)).any(dim=2).sum()
+            self.looka_tot[1] += T * k
+        if mli + 1 < L["n_main"]:
+            cfg, nxt, K = self.cfg, L["layers"][mli + 1], L["K"]
+            lg = self.ws.get("looka.logits", (T, cfg.num_experts), torch.float32)
+            self._router_logits(hb, nxt, lg)
+            pid = self.ws.get("looka.ids", (T, K), torch.int32)
+            pw = self.ws.get("looka.w", (T, K), torch.float32)
+            self.C.router_topk(lg, nxt.router_bias, K, cfg.router == "sigmoid", cfg.n_group, cfg.topk_group,
+                               cfg.norm_topk_prob, cfg.routed_scaling, pid, pw)
+            pred.copy_(pid)
+            if self.pilot_log is not None:
+                self.pilot_log[mli + 1, :T].copy_(pid)
 
     def attach_delta_tier(self, tier):
         """Serve experts that hold a delta slot at FP4 precision (decode GEMVs)."""
@@ -816,6 +872,7 @@ class NativeRunner:
             C.moe_route_fused(hb, self._router_w(lw), logits, lw.router_bias, k, cfg.router == "sigmoid",
                               cfg.n_group, cfg.topk_group, cfg.norm_topk_prob, cfg.routed_scaling, ids, wts, MB,
                               rank, stok, posof, pairs, npairs, cnt, self.status, max(e_lo, 0), E_loc if ep else 0)
+            self._looka_step(mli, hb, ids, ctx)
             self._ensure_experts(mli, ids)
             y2 = self._moe_gemv_pairs(h2q, h2s, stok, pairs, npairs, ex, R, MB, mli)
         else:
@@ -828,6 +885,7 @@ class NativeRunner:
                 pi, pw = apply_topp(ids, wts, topp, self.ecfg.moet.topp_min)
                 ids.copy_(pi)
                 wts.copy_(pw)
+            self._looka_step(mli, hb, ids, ctx)
             self._ensure_experts(mli, ids)
             if use_tc:
                 y2, posof = self._moe_tc(h2q, h2s, ids, ex, R, T, E_loc, e_lo)

@@ -225,7 +225,7 @@ class LLM:
                 self.runner.set_pp_group(pp_group)
                 self.ecfg.cuda_graphs = False      # pipeline stages run eager steps (p2p per step)
             self.cache = self.replay = None
-            self.spec_guard = self.affinity = None
+            self.spec_guard = self.affinity = self.pilot = None
             self._spec_draft = True
             slots = expert_cache_slots
             if not slots and self.ecfg.moet.base_cache_gb > 0:
@@ -394,6 +394,13 @@ class LLM:
                                    fp_max=m.fp_max,
                                    miss_tol=m.base_miss_tol)
         self.affinity = DraftAffinity(self.cache) if m.prefetch and self.k > 0 else None
+        self.pilot = None
+        if m.looka or m.pilot:
+            # router lookahead in the decode graph; PILOT prefetches its predictions
+            from ..residency import Pilot
+            self.runner.enable_looka(m.pilot_k, m.pilot, self._bucket(self.ecfg.max_num_seqs) * (self.k + 1))
+            if m.pilot:
+                self.pilot = Pilot(self.cache, self.runner.pilot_log, m.pilot_cap, m.pilot_min_replay)
 
     # ------------------------------------------------------------------ API
     def _normalize(self, prompts) -> List[List[int]]:
@@ -803,6 +810,9 @@ class LLM:
                               fetched_rows=self.cache.stats["fetched_rows"] - f0)
                 if self.spec_guard is not None:
                     self._spec_draft = self.spec_guard.observe(n_rep > 0)
+                if getattr(self, "pilot", None) is not None:
+                    self.pilot.observe(n_rep > 0)
+                    self.pilot.consume()
                 if self.affinity is not None and draft:
                     # learn token -> experts from this step's verify rows, then prefetch what the
                     # next step's drafts routed to before (asynchronously, off the decode stream)
@@ -843,6 +853,10 @@ class LLM:
                 if self._emit(r, pin_out[i, :a + 1].tolist(), lg):
                     self._finish_row(r, rows)
         self.stats = dict(steps=steps, accepted=accepted, decode_s=t_decode, bucket=B)
+        if getattr(runner, "_looka", None) is not None:
+            self.stats["looka_recall"] = runner.looka_recall()
+        if getattr(self, "pilot", None) is not None:
+            self.stats["pilot"] = dict(self.pilot.stats)
 
     def _run_native_ep(self, reqs):
         """GPU engine loop under data-parallel attention + expert parallelism.  Every rank of

@@ -1,7 +1,7 @@
 """Expert residency: host stores, the persistent planes cache, the GPU expert
 cache with in-graph miss counting and replay, the confidence gate, the
 speculation guard and the routing prefetchers."""
-from .control import (ConfidenceGate, DraftAffinity, LookaheadPrefetcher, ReplayEngine, SpecGuard,  # noqa: F401
+from .control import (ConfidenceGate, DraftAffinity, LookaheadPrefetcher, Pilot, ReplayEngine, SpecGuard,  # noqa: F401
                       gate_fire_floor, pp_gate_barrier, gate_promote_consensus)
 from .identity import checkpoint_id, identity_fields, rank_suffix  # noqa: F401
 from .planes_cache import PlanesCache  # noqa: F401

@@ -240,6 +240,49 @@ class LookaheadPrefetcher:
             self.cache.request_prefetch(pairs)
 
 
+class Pilot:
+    """Host half of the router-lookahead prefetch (PILOT).  The decode graph writes, per
+    main-stack MoE layer L + 1, the experts layer L + 1's router picks from layer L's MoE
+    input (``log`` [layers, rows, K], -1 = empty).  After a step this reads the log once
+    (and clears it, so a stale prediction is never fetched twice), and while the pool is
+    cold -- the replay EMA at or above ``min_replay`` percent -- asks the cache to prefetch
+    up to ``cap`` predicted non-resident experts off the decode stream.  On a warm pool the
+    step's own misses cover the working set and predictions would only churn slots.
+    (Reference: the PILOT consumer, patch P:11940-12006.)"""
+
+    def __init__(self, cache: ExpertCache, log: torch.Tensor, cap: int = 32, min_replay: float = 30.0,
+                 alpha: float = 0.05):
+        self.cache, self.log, self.cap = cache, log, int(cap)
+        self.min_replay, self.alpha = float(min_replay), float(alpha)
+        self.ema = 1.0                     # a fresh pool is cold
+        self.stats = collections.Counter()
+
+    def observe(self, replayed: bool) -> None:
+        self.ema += self.alpha * (float(replayed) - self.ema)
+
+    def consume(self) -> int:
+        """-> experts requested this step."""
+        host = self.log.to("cpu", copy=True)
+        self.log.fill_(-1)
+        if 100.0 * self.ema < self.min_replay:
+            self.stats["warm_skips"] += 1
+            return 0
+        E = self.cache.E
+        flat = host.reshape(host.shape[0], -1)
+        pairs: List[Tuple[int, int]] = []
+        seen = set()
+        for li in range(flat.shape[0]):
+            for e in torch.unique(flat[li]).tolist():
+                if 0 <= e < E and (li, e) not in seen and not self.cache.resident(li, e):
+                    seen.add((li, e))
+                    pairs.append((li, int(e)))
+        pairs = pairs[: self.cap]
+        if pairs:
+            self.stats["requested"] += len(pairs)
+            self.cache.request_prefetch(pairs)
+        return len(pairs)
+
+
 class DraftAffinity:
     """token -> per-layer expert sets learned from routing; prefetch for drafted tokens."""
 
