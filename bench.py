@@ -176,6 +176,16 @@ def main():
     e2e_tok_s = (len(outs[0].outputs[0].token_ids) - 1) / maxr(m["e2e_s"] - m["ttft_s"])
 
     extra, errors = {}, {}
+    if world > 1 and not args.ep:
+        # correctness gate across the TP ranks: every rank emits the whole sequence, and the
+        # same greedy tokens on every rank are the condition for the timed steps to mean
+        # anything (diverging ranks would write their KV shards for different sequences)
+        ids = torch.full((n_tok,), -1, dtype=torch.int64, device="cuda")
+        mine = torch.tensor(outs[0].outputs[0].token_ids[:n_tok], dtype=torch.int64)
+        ids[:mine.numel()] = mine.to("cuda")
+        every = [torch.empty_like(ids) for _ in range(world)]
+        dist.all_gather(every, ids)
+        extra["tp_ranks_same_tokens"] = all(torch.equal(every[0], x) for x in every[1:])
 
     def secondary(name, fn):
         """A secondary measurement that fails (the same way on every rank) is reported as an
