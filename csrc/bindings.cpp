@@ -104,6 +104,12 @@ void kv_prep(torch::Tensor kva, int64_t lat, int64_t rope, torch::Tensor norm_w,
 void mla_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kr, torch::Tensor cu_seqlens, int64_t max_len,
                  double scale, c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_s,
                  c10::optional<torch::Tensor> out_bf16, c10::optional<torch::Tensor> cu_seqlens_k);
+// trellis.cu
+void trellis_rot_in(torch::Tensor x, torch::Tensor src, torch::Tensor eid, torch::Tensor su, torch::Tensor out);
+void trellis_rot_out(torch::Tensor z, torch::Tensor eid, torch::Tensor sv, c10::optional<torch::Tensor> scale,
+                     torch::Tensor out);
+void trellis_gemv(torch::Tensor xr, torch::Tensor trellis, torch::Tensor experts, torch::Tensor row_map,
+                  torch::Tensor z, int64_t K, int64_t L, bool mad, double inv_rms, int64_t maxr);
 // hyper_conn.cu
 void hc_mix(torch::Tensor xs, c10::optional<torch::Tensor> upd, c10::optional<torch::Tensor> post,
             c10::optional<torch::Tensor> comb, c10::optional<torch::Tensor> fn, c10::optional<torch::Tensor> part);
@@ -208,6 +214,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_combine", &mla_combine);
   m.def("q_prep", &q_prep);
   m.def("kv_prep", &kv_prep);
+  m.def("trellis_rot_in", &trellis_rot_in);
+  m.def("trellis_rot_out", &trellis_rot_out, py::arg("z"), py::arg("eid"), py::arg("sv"), py::arg("scale"),
+        py::arg("out"));
+  m.def("trellis_gemv", &trellis_gemv);
   m.def("hc_mix", &hc_mix, py::arg("xs"), py::arg("upd") = py::none(), py::arg("post") = py::none(),
         py::arg("comb") = py::none(), py::arg("fn") = py::none(), py::arg("part") = py::none());
   m.def("hc_apply", &hc_apply, py::arg("xs"), py::arg("part"), py::arg("base"), py::arg("scale"), py::arg("eps"),

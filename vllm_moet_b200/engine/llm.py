@@ -58,7 +58,7 @@ class LLM:
                  dspark: Optional[dict] = None, enable_prefix_caching: bool = False,
                  prefix_block_size: int = 16, enable_chunked_prefill: bool = False,
                  max_num_batched_tokens: Optional[int] = None, tp_attention: Optional[str] = None,
-                 **model_overrides):
+                 trellis_pack: Optional[str] = None, **model_overrides):
         from ..models.loader import hf_config, is_checkpoint_dir, load_weights
         ckpt = model if is_checkpoint_dir(model) else None
         if ckpt is not None:
@@ -85,6 +85,9 @@ class LLM:
         self._dcp = None
         if self.device.type == "cuda" and sp_group is not None and (enable_prefix_caching or enable_chunked_prefill):
             raise NotImplementedError("GPU SP prefill: no prefix caching or chunked prefill")
+        if self.device.type == "cuda" and (trellis_pack or os.environ.get("VLLM_MOE_W2_EXL3_PACK")):
+            raise NotImplementedError("trellis base tier: served by the CPU engine; on a GPU its kernels run through "
+                                      "residency.trellis_tier.TrellisBaseTier.forward_topk")
         self._sp_group = sp_group
         self._ep_group = ep_group
         if speculative_method not in ("mtp", "dspark", "dflash", "eagle3"):
@@ -253,6 +256,23 @@ class LLM:
                                       ep_group=ep_group,
                                       dspark=(dspark or {}) if speculative_method == "dspark" else None,
                                       prefix_block=prefix_block_size if enable_prefix_caching else 0)
+            trellis_pack = trellis_pack or os.environ.get("VLLM_MOE_W2_EXL3_PACK") or None
+            self.trellis = None
+            if trellis_pack:
+                self.trellis = self._attach_trellis(trellis_pack, tp_group, pp_group, sp_group, dcp_group, ep_group)
+
+    def _attach_trellis(self, pack_dir, *groups):
+        """Serve the routed experts of every MoE layer that has a pack in ``pack_dir`` from
+        the trellis base tier (single rank, unsharded experts)."""
+        from ..residency.trellis_tier import TrellisBaseTier, pack_path
+        if any(g is not None for g in groups):
+            raise NotImplementedError("trellis base tier: one rank with every expert (no TP / PP / SP / DCP / EP)")
+        layers = [li for li, lw in enumerate(self.mw.layers) if lw.is_moe and os.path.exists(pack_path(pack_dir, li))]
+        if not layers:
+            raise FileNotFoundError(f"no trellis packs (exl3-lNN.safetensors) for the MoE layers in {pack_dir}")
+        tier = TrellisBaseTier(pack_dir, layers, device=self.device, act_limit=self.mw.cfg.swiglu_limit)
+        self.runner.moe_impl = tier.moe_fn(self.mw)
+        return tier
 
     def _attach_tracing(self):
         """Prefill span timers, routing capture, delta trace / dump and the gate JSONL

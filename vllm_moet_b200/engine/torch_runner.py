@@ -52,6 +52,7 @@ class TorchRunner:
         self.sp_group = sp_group        # sequence-parallel prefill ranks: prompt chunks, gathered MLA latents
         self.dcp_group = dcp_group      # decode-context-parallel ranks: KV interleaved by position, LSE merge
         self.dcp_interleave = dcp_interleave
+        self.moe_impl = None            # routed-expert function replacing the MoE block (e.g. the trellis tier)
         self.ep_group = ep_group        # expert parallelism over data-parallel ranks (all-to-all MoE)
         if dspark is not None:
             if self.dspark["drafter"] is None:
@@ -70,6 +71,8 @@ class TorchRunner:
 
     def _ctx(self):
         import contextlib
+        if self.moe_impl is not None:        # an alternative routed-expert tier (one rank)
+            return ref.moe_context(self.moe_impl)
         if self.ep_group is not None:
             from ..parallel.ep import ep_moe_block
             g = self.ep_group
