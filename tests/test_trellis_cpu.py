@@ -253,3 +253,65 @@ def test_pack_builder_cli(tmp_path, capsys):
     assert 0 < rec["rel_err_w13_e0"] < 0.5 and 0 < rec["rel_err_w2_e0"] < 0.4
     tier = tt.TrellisBaseTier(str(tmp_path), [1])
     assert (tier.w13_k, tier.w2_k, tier.L, tier.codebook) == (2, 3, 6, "1mad")
+
+
+def test_delta_pool_serves_base_plus_residual(tiny_tier):
+    from vllm_moet_b200.models.reference import swiglu
+    llm, d, layers = tiny_tier
+    cfg = llm.mw.cfg
+    li = layers[0]
+    tier = tt.TrellisBaseTier(d, layers, act_limit=cfg.swiglu_limit)
+    pool = tt.TrellisDeltaPool(tier, slots=2, dk13=3, dk2=3, L=8)
+    true = [llm.mw.layers[li].experts.dequant_expert(e) for e in range(cfg.num_experts)]
+    for e in (1, 4):
+        assert pool.promote(li, e, *true[e]) in (0, 1)
+    # the pooled experts are served closer to their true weights than by the base alone
+    for e in (1, 4):
+        b13, b2 = tier.dequant_expert(li, e)
+        p13, p2 = pool.dequant_expert(li, e)
+        assert (p13 - true[e][0]).norm() < 0.5 * (b13 - true[e][0]).norm()
+        assert (p2 - true[e][1]).norm() < 0.5 * (b2 - true[e][1]).norm()
+    assert torch.equal(pool.dequant_expert(li, 0)[0], tier.dequant_expert(li, 0)[0])
+    torch.manual_seed(2)
+    T = 5
+    x = torch.randn(T, cfg.hidden)
+    ids = torch.stack([torch.randperm(cfg.num_experts)[:cfg.top_k] for _ in range(T)])
+    ids[0, 0], ids[1, 1] = 1, 4
+    w = torch.rand(T, cfg.top_k)
+    y = tier.forward_topk(li, x, ids, w, delta=pool)
+    want = torch.zeros(T, cfg.hidden)
+    for t in range(T):
+        for j in range(cfg.top_k):
+            w13, w2 = pool.dequant_expert(li, int(ids[t, j]))
+            want[t] += w[t, j] * (swiglu(x[t:t + 1] @ w13.t(), cfg.swiglu_limit) @ w2.t())[0]
+    assert torch.allclose(y, want, rtol=1e-4, atol=1e-5)
+    # FIFO eviction once the slots are full; re-promotion keeps the expert's slot
+    s4 = int(pool.slot_of[li][4])
+    assert pool.promote(li, 4, *true[4]) == s4
+    pool.promote(li, 6, *true[6])                 # evicts expert 1, the oldest promotion
+    assert int(pool.slot_of[li][1]) == -1 and int(pool.slot_of[li][6]) >= 0
+    assert pool.stats == {"promoted": 4, "evicted": 1}
+    pool.evict(li, 6)
+    assert int(pool.slot_of[li][6]) == -1
+    y0 = tier.forward_topk(li, x, ids, w, delta=pool)     # only expert 4 is still pooled
+    want0 = tier.forward_topk(li, x, ids, w)
+    m = (ids == 4)
+    assert torch.allclose(y0[~m.any(1)], want0[~m.any(1)], rtol=1e-5, atol=1e-6)
+    assert not torch.allclose(y0[m.any(1)], want0[m.any(1)], rtol=1e-3, atol=1e-5)
+
+
+def test_engine_with_delta_pool_matches_oracle(tiny_tier):
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.engine.llm import LLM
+    from vllm_moet_b200.models import reference as ref
+    _, d, layers = tiny_tier
+    llm = LLM("tiny-moe", device="cpu", num_speculative_tokens=2, max_model_len=128, trellis_pack=d)
+    pool = tt.TrellisDeltaPool(llm.trellis, slots=3, L=8)
+    for li in layers:
+        for e in range(3):
+            pool.promote(li, e, *llm.mw.layers[li].experts.dequant_expert(e))
+    llm.trellis.attach_delta(pool)
+    p = list(range(40, 64))
+    out = llm.generate([p], SamplingParams(max_tokens=8, ignore_eos=True))[0].outputs[0].token_ids
+    with ref.moe_context(llm.trellis.moe_fn(llm.mw)):
+        assert out == ref.greedy_generate(llm.mw, p, 8)

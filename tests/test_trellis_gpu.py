@@ -83,3 +83,27 @@ def test_trellis_tier_gpu_matches_cpu(tmp_path, K13, K2, L, codebook):
         # deterministic: fixed-order sums everywhere
         again = gpu.forward_topk(0, x.cuda(), ids.cuda(), w.cuda())
         assert torch.equal(again, gpu.forward_topk(0, x.cuda(), ids.cuda(), w.cuda()))
+
+
+def test_trellis_delta_pool_gpu_matches_cpu(tmp_path):
+    E, H, I = 8, 256, 128
+    _random_pack(tmp_path, E, H, I, 2, 2, 12, "3inst", seed=11)
+    g = torch.Generator().manual_seed(4)
+    true = [(torch.randn(2 * I, H, generator=g) * 0.01, torch.randn(H, I, generator=g) * 0.01) for _ in range(3)]
+    tiers = {}
+    for dev in ("cpu", "cuda"):
+        t = tt.TrellisBaseTier(str(tmp_path), [0], device=dev, act_limit=7.0)
+        pool = tt.TrellisDeltaPool(t, slots=2, dk13=2, dk2=3, L=8)
+        for e in (2, 5, 7):                       # the third promotion evicts expert 2
+            pool.promote(0, e, *true[(2, 5, 7).index(e)])
+        tiers[dev] = (t, pool)
+    assert torch.equal(tiers["cuda"][1].slot_of[0], tiers["cpu"][1].slot_of[0])
+    for T in (1, 4):
+        x = torch.randn(T, H, generator=g)
+        ids = torch.stack([torch.randperm(E, generator=g)[:4] for _ in range(T)])
+        ids[0] = torch.tensor([5, 7, 0, 2])        # both pooled experts, one evicted, one never pooled
+        w = torch.rand(T, 4, generator=g)
+        want = tiers["cpu"][0].forward_topk(0, x, ids, w, delta=tiers["cpu"][1])
+        got = tiers["cuda"][0].forward_topk(0, x.cuda(), ids.cuda(), w.cuda(), delta=tiers["cuda"][1])
+        torch.cuda.synchronize()
+        assert _rel(got, want) < 1e-4, T

@@ -183,62 +183,96 @@ class TrellisBaseTier:
             u = u.clamp(-self.act_limit, self.act_limit)
         return F.silu(g) * u
 
+    def _stream(self, li: int) -> dict:
+        """The base stream of layer li: trellis tensors indexed by expert id."""
+        return dict(st=self.layers[li], K13=self.w13_k, K2=self.w2_k, L=self.L, codebook=self.codebook,
+                    inv_rms=self.inv_rms, slot_of=None, qcache=self._q, key=("base", li))
+
     @torch.no_grad()
     def forward_topk(self, li: int, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
-                     fp4_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+                     fp4_mask: Optional[torch.Tensor] = None,
+                     delta: Optional["TrellisDeltaPool"] = None) -> torch.Tensor:
         """x [T, H], ids [T, k], weights [T, k] -> routed output [T, H] fp32 without the
-        pairs marked in fp4_mask [T, k] (served by another tier)."""
+        pairs marked in fp4_mask [T, k] (served by another tier).
+
+        With a delta pool, the pairs whose expert holds a slot are served base + delta: the
+        delta's gate / up outputs are added before the SwiGLU and its down output after
+        (weight-level additivity, (Wb + D) x = Wb x + D x), the reference's unified Δ-pool
+        semantics (forward_topk_unified, patch P:10796-10818)."""
         w = weights.float()
         if fp4_mask is not None:
             w = w.masked_fill(fp4_mask, 0.0)
+        streams = [self._stream(li)]
+        if delta is not None and li in delta.layers:
+            streams.append(delta._stream(li))
         if x.is_cuda:
-            return self._forward_native(li, x, ids, w)
-        return self._forward_ref(li, x, ids, w)
+            return self._forward_native(x, ids, w, streams)
+        return self._forward_ref(x, ids, w, streams)
 
-    def _forward_ref(self, li, x, ids, w):
+    def _swiglu_sum(self, parts_g, parts_u):
+        return self._swiglu(sum(parts_g), sum(parts_u))
+
+    def _forward_ref(self, x, ids, w, streams):
         out = torch.zeros(x.shape[0], self.H, dtype=torch.float32)
+
+        def lin(sm, row, inp, name):
+            K = sm["K2"] if name == "w2" else sm["K13"]
+            key = sm["key"] + (row, name)
+            if key not in sm["qcache"]:
+                sm["qcache"][key] = tf.decode_q(sm["st"][f"{name}.trellis"][row].cpu(), K, sm["L"], sm["codebook"])
+            t = {p: sm["st"][f"{name}.{p}"][row].cpu() for p in ("trellis", "suh", "svh")}
+            return tf.apply_linear(inp, t, K, sm["L"], sm["codebook"], q=sm["qcache"][key])
         for e in torch.unique(ids).tolist():
             rows, slot = (ids == e).nonzero(as_tuple=True)
             xe = x[rows].float().cpu()
-
-            def lin(inp, name):
-                key = (li, e, name)
-                if key not in self._q:
-                    self._q[key] = tf.decode_q(self.layers[li][f"{name}.trellis"][e].cpu(), self._K(name),
-                                               self.L, self.codebook)
-                t = {p: v.cpu() for p, v in self._t(li, e, name).items()}
-                return tf.apply_linear(inp, t, self._K(name), self.L, self.codebook, q=self._q[key])
-            h = self._swiglu(lin(xe, "w1"), lin(xe, "w3"))
-            out.index_add_(0, rows.cpu(), lin(h, "w2") * w[rows, slot, None].cpu())
+            live = []
+            for sm in streams:
+                row = e if sm["slot_of"] is None else int(sm["slot_of"][e])
+                if row >= 0:
+                    live.append((sm, row))
+            h = self._swiglu_sum([lin(sm, r, xe, "w1") for sm, r in live], [lin(sm, r, xe, "w3") for sm, r in live])
+            y = sum(lin(sm, r, h, "w2") for sm, r in live)
+            out.index_add_(0, rows.cpu(), y * w[rows, slot, None].cpu())
         return out.to(x.device)
 
-    def _forward_native(self, li, x, ids, w):
+    def _forward_native(self, x, ids, w, streams):
         from ..ops import native
         C = native()
-        st = self.layers[li]
         T, k = ids.shape
         P = T * k
-        experts, row_map = group_pairs(ids)
-        eid = ids.reshape(P).to(torch.int32)
-        src = torch.arange(P, device=x.device, dtype=torch.int32) // k
-        maxr = min(T, 8)
+        dev = x.device
         xf = x.float().contiguous()
+        src = torch.arange(P, device=dev, dtype=torch.int32) // k
+        own = torch.arange(P, device=dev, dtype=torch.int32)
+        wp = w.reshape(P).contiguous()
+        plans = []
+        for sm in streams:
+            if sm["slot_of"] is None:     # base: every pair, groups of distinct experts per token
+                rid, sel, maxr = ids, None, min(T, 8)
+            else:                         # delta: pooled pairs; the others read slot 0, weighted 0
+                so = sm["slot_of"].to(dev)[ids.long()]
+                sel = (so >= 0).float().reshape(P).contiguous()
+                rid, maxr = so.clamp_min(0), 8
+            experts, row_map = group_pairs(rid)
+            plans.append((sm, rid.reshape(P).to(torch.int32).contiguous(), experts, row_map, sel, maxr))
 
-        def proj(inp, src_rows, name, scale=None):
-            K = self._K(name)
-            kin = st[f"{name}.suh"].shape[1]
-            n = st[f"{name}.svh"].shape[1]
-            xr = torch.empty(P, kin, dtype=torch.float32, device=x.device)
+        def proj(plan, inp, src_rows, name, scale):
+            sm, eid, experts, row_map, _, maxr = plan
+            st = sm["st"]
+            K = sm["K2"] if name == "w2" else sm["K13"]
+            kin, n = st[f"{name}.suh"].shape[1], st[f"{name}.svh"].shape[1]
+            xr = torch.empty(P, kin, dtype=torch.float32, device=dev)
             C.trellis_rot_in(inp, src_rows, eid, st[f"{name}.suh"], xr)
-            z = torch.empty(P, n, dtype=torch.float32, device=x.device)
-            C.trellis_gemv(xr, st[f"{name}.trellis"], experts, row_map, z, K, self.L,
-                           self.codebook == "1mad", self.inv_rms, maxr)
+            z = torch.empty(P, n, dtype=torch.float32, device=dev)
+            C.trellis_gemv(xr, st[f"{name}.trellis"], experts, row_map, z, K, sm["L"], sm["codebook"] == "1mad",
+                           sm["inv_rms"], maxr)
             y = torch.empty_like(z)
             C.trellis_rot_out(z, eid, st[f"{name}.svh"], scale, y)
             return y
-        h = self._swiglu(proj(xf, src, "w1"), proj(xf, src, "w3")).contiguous()
-        own = torch.arange(P, device=x.device, dtype=torch.int32)
-        y = proj(h, own, "w2", w.reshape(P).contiguous())
+        g = sum(proj(pl, xf, src, "w1", pl[4]) for pl in plans)
+        u = sum(proj(pl, xf, src, "w3", pl[4]) for pl in plans)
+        h = self._swiglu(g, u).contiguous()
+        y = sum(proj(pl, h, own, "w2", wp if pl[4] is None else wp * pl[4]) for pl in plans)
         return y.view(T, k, self.H).sum(1)              # fixed order over k: deterministic
 
     def moe_fn(self, mw):
@@ -257,14 +291,115 @@ class TrellisBaseTier:
             if ref._TOPP[0] > 0:
                 from ..models.moe_policy import apply_topp
                 ids, w = apply_topp(ids, w, *ref._TOPP)
-            out = self.forward_topk(li, h, ids, w).to(h.device)
+            out = self.forward_topk(li, h, ids, w, delta=getattr(self, "delta", None)).to(h.device)
             if lw.shared_gate_up is not None:
                 out = out + ref.swiglu(h.float() @ lw.shared_gate_up.dequant().t(), cfg.swiglu_limit) \
                     @ lw.shared_down.dequant().t()
             return out
         return fn
 
+    def attach_delta(self, pool: "TrellisDeltaPool"):
+        """Serve this tier's layers base + delta through ``moe_fn``."""
+        self.delta = pool
+
     def describe(self) -> str:
         return json.dumps({"layers": sorted(self.layers), "E": self.E, "H": self.H, "I": self.I, "L": self.L,
                            "codebook": self.codebook, "w13_k": self.w13_k, "w2_k": self.w2_k,
                            "bytes": self.total_bytes()})
+
+
+class TrellisDeltaPool:
+    """Correction slots over the trellis base tier (the reference's EXL3 Δ pool,
+    ``delta_slot_geom`` / ``delta_ptr_tables``, patch P:10411-10446): a promoted expert's
+    residual ``W_true - W_base`` (the base as the tier serves it) is trellis-coded into a
+    slot at its own bits (``dk13`` / ``dk2``) and codebook (1MAD by default, the base packs
+    use 3INST), and the tier then serves that expert base + delta.  Slot tensors are
+    stacked [slots, ...] per layer on the tier's device; ``slot_of[li]`` maps expert -> slot
+    (-1: not pooled).  Promotion reuses the slot of an expert already pooled, takes a free
+    one, or evicts the oldest promotion (FIFO)."""
+
+    def __init__(self, tier: TrellisBaseTier, slots: int, layers: Optional[Iterable[int]] = None,
+                 dk13: int = 2, dk2: int = 2, L: Optional[int] = None, codebook: str = "1mad", seed: int = 1):
+        if slots < 1:
+            raise ValueError("delta pool needs at least one slot")
+        self.tier, self.slots = tier, int(slots)
+        self.dk13, self.dk2 = dk13, dk2
+        self.L = L if L is not None else tier.L
+        self.codebook, self.seed = codebook, seed
+        self.inv_rms = 1.0 / tf.codebook_rms(self.L, codebook)
+        H, I, dev = tier.H, tier.I, tier.dev
+        self.layers: Dict[int, Dict[str, torch.Tensor]] = {}
+        self.slot_of: Dict[int, torch.Tensor] = {}
+        self.order: Dict[int, list] = {}
+        self._q: Dict[tuple, torch.Tensor] = {}
+        for li in (layers if layers is not None else tier.layers):
+            st = {}
+            for name, (n, kin, K) in (("w1", (I, H, dk13)), ("w3", (I, H, dk13)), ("w2", (H, I, dk2))):
+                st[f"{name}.trellis"] = torch.zeros(self.slots, kin // 16, n // 16, 16 * K, dtype=torch.int16,
+                                                    device=dev)
+                st[f"{name}.suh"] = torch.ones(self.slots, kin, dtype=torch.float16, device=dev)
+                st[f"{name}.svh"] = torch.zeros(self.slots, n, dtype=torch.float16, device=dev)
+            self.layers[li] = st
+            self.slot_of[li] = torch.full((tier.E,), -1, dtype=torch.int32)
+            self.order[li] = []
+        self.stats = {"promoted": 0, "evicted": 0}
+
+    def _stream(self, li: int) -> dict:
+        return dict(st=self.layers[li], K13=self.dk13, K2=self.dk2, L=self.L, codebook=self.codebook,
+                    inv_rms=self.inv_rms, slot_of=self.slot_of[li], qcache=self._q, key=("delta", li))
+
+    def promote(self, li: int, e: int, w13: torch.Tensor, w2: torch.Tensor, device=None) -> int:
+        """Code expert e's residual against the base tier into a slot; returns the slot.
+        ``w13`` [2I, H] (gate rows first) and ``w2`` [H, I] are the expert's true weights."""
+        so = self.slot_of[li]
+        s = int(so[e])
+        if s < 0:
+            used = set(int(v) for v in so.tolist() if v >= 0)
+            free = [i for i in range(self.slots) if i not in used]
+            if free:
+                s = free[0]
+            else:
+                old = self.order[li].pop(0)
+                s = int(so[old])
+                so[old] = -1
+                self.stats["evicted"] += 1
+        else:
+            self.order[li].remove(e)
+        b13, b2 = self.tier.dequant_expert(li, e)
+        I = w13.shape[0] // 2
+        res = {"w1": w13[:I].float().cpu() - b13[:I], "w3": w13[I:].float().cpu() - b13[I:],
+               "w2": w2.float().cpu() - b2}
+        st = self.layers[li]
+        for pi, name in enumerate(("w1", "w3", "w2")):
+            K = self.dk2 if name == "w2" else self.dk13
+            t = tf.quantize_linear(res[name], K, self.L, self.codebook,
+                                   seed=(self.seed * 1000003 + li * 10007 + e * 31 + pi) & 0x7FFFFFFF, device=device)
+            for part, v in t.items():
+                st[f"{name}.{part}"][s].copy_(v.to(st[f"{name}.{part}"].device))
+            for key in [k_ for k_ in self._q if k_[:2] == ("delta", li) and k_[2] == s]:
+                del self._q[key]
+        so[e] = s
+        self.order[li].append(e)
+        self.stats["promoted"] += 1
+        return s
+
+    def evict(self, li: int, e: int) -> None:
+        so = self.slot_of[li]
+        if int(so[e]) >= 0:
+            so[e] = -1
+            self.order[li].remove(e)
+            self.stats["evicted"] += 1
+
+    def dequant_expert(self, li: int, e: int):
+        """-> (w13, w2) the tier serves for expert e with the pool: base + delta (or base)."""
+        b13, b2 = self.tier.dequant_expert(li, e)
+        s = int(self.slot_of[li][e])
+        if s < 0:
+            return b13, b2
+        st = self.layers[li]
+
+        def d(name):
+            K = self.dk2 if name == "w2" else self.dk13
+            t = {p: st[f"{name}.{p}"][s].cpu() for p in ("trellis", "suh", "svh")}
+            return tf.dequant_linear(t, K, self.L, self.codebook)
+        return b13 + torch.cat([d("w1"), d("w3")]), b2 + d("w2")
