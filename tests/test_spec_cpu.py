@@ -265,3 +265,17 @@ def test_eagle3_drafts_from_aux_hidden_states():
         LLM("tiny-moe", device="cuda", speculative_method="eagle3", tensor_parallel_size=2)
     with pytest.raises(NotImplementedError):
         LLM("tiny-moe", device="cuda", speculative_method="eagle3", hc_mult=4)
+
+
+def test_dspark_swa_indices_batch_equals_scalar():
+    from vllm_moet_b200.spec import swa_indices, swa_indices_batch
+    lens = torch.tensor([0, 1, 5, 255, 256, 257, 1000, 5000])
+    for block, window, width in ((4, 256, 512), (8, 600, 640), (3, 16, 24)):
+        got = swa_indices_batch(lens, block, window, width)
+        assert got.shape == (len(lens), width) and got.dtype == torch.int32
+        for b, c in enumerate(lens.tolist()):
+            ref = swa_indices(c, block, window, min_width=1, align=1)
+            want = torch.full((width,), -1, dtype=torch.int32)
+            n = min(width, ref.numel())
+            want[:n] = ref[:n]
+            assert torch.equal(got[b], want), (c, block, window)

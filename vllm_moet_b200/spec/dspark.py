@@ -106,3 +106,16 @@ def swa_indices(context_len: int, block_len: int, window: int, min_width: int = 
     out = torch.full((width,), -1, dtype=torch.int32)
     out[: idx.numel()] = idx
     return out
+
+
+def swa_indices_batch(context_lens: torch.Tensor, block_len: int, window: int, width: int) -> torch.Tensor:
+    """``swa_indices`` for a batch of draft blocks at one fixed width, as tensor ops on the
+    lengths' device (no host loop, no data-dependent shapes: usable inside a captured
+    step).  context_lens [B] -> [B, width] int32; row b equals ``swa_indices(context_lens[b],
+    block_len, window)`` truncated or -1-padded to ``width``."""
+    c = context_lens.to(torch.int64).view(-1, 1)
+    start = (c - window).clamp_min(0)
+    n_ctx = c - start                                   # trailing context positions kept
+    j = torch.arange(width, device=context_lens.device, dtype=torch.int64).view(1, -1)
+    out = torch.where(j < n_ctx, start + j, c + (j - n_ctx))
+    return torch.where(j < n_ctx + block_len, out, torch.full_like(out, -1)).to(torch.int32)
