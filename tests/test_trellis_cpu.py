@@ -315,3 +315,33 @@ def test_engine_with_delta_pool_matches_oracle(tiny_tier):
     out = llm.generate([p], SamplingParams(max_tokens=8, ignore_eos=True))[0].outputs[0].token_ids
     with ref.moe_context(llm.trellis.moe_fn(llm.mw)):
         assert out == ref.greedy_generate(llm.mw, p, 8)
+
+
+def test_pack_builder_codes_checkpoint_experts_from_the_source(tmp_path, capsys):
+    import json
+    import sys as _sys
+    _sys.path.insert(0, str(__import__("pathlib").Path(__file__).parent))
+    from test_loader_cpu import _make_ckpt
+    from vllm_moet_b200.engine.llm import LLM
+    from vllm_moet_b200.tools.build_trellis_pack import main
+    ck = str(tmp_path / "ckpt")
+    _make_ckpt(ck, quant=True)
+    out = str(tmp_path / "packs")
+    assert main([out, "--checkpoint", ck, "--L", "8", "--w13-k", "3", "--w2-k", "3"]) == 0
+    recs = [json.loads(x) for x in capsys.readouterr().out.strip().splitlines() if x.startswith("{")]
+    llm = LLM(ck, device="cpu", num_speculative_tokens=0, max_model_len=64)
+    moe = [li for li, lw in enumerate(llm.mw.layers) if lw.is_moe]
+    assert [r["layer"] for r in recs] == moe
+    tier = tt.TrellisBaseTier(out, moe)
+    for li in moe:
+        src13, src2 = next(tt.checkpoint_experts(ck, li, 1))
+        t13, t2 = tier.dequant_expert(li, 0)
+        c13, c2 = llm.mw.layers[li].experts.dequant_expert(0)       # the engine's 2-bit copy
+        # 3-bit trellis from the source beats the 2-bit codebook on the same weights
+        assert (t13 - src13).norm() < (c13 - src13).norm() and (t2 - src2).norm() < (c2 - src2).norm()
+    # the tier serves the checkpoint through the engine
+    eng = LLM(ck, device="cpu", num_speculative_tokens=0, max_model_len=64, trellis_pack=out)
+    assert sorted(eng.trellis.layers) == moe
+    assert len(eng.generate([[5, 6, 7]], __import__("vllm_moet_b200").SamplingParams(max_tokens=3,
+                                                                                 ignore_eos=True))[0]
+               .outputs[0].token_ids) == 3

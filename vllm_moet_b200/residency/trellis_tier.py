@@ -84,6 +84,30 @@ def write_model_packs(mw, pack_dir: str, layers: Optional[Iterable[int]] = None,
     return done
 
 
+def checkpoint_experts(path: str, li: int, num_experts: int):
+    """The routed experts of layer li as the checkpoint stores them (bf16 / FP8 / NVFP4
+    dequantised exactly), ``(w13 [2I, H], w2 [H, I])`` per expert: the source a trellis
+    pack should be coded from, rather than another quantisation of it."""
+    from ..models.loader import CheckpointReader
+    rd = CheckpointReader(path)
+    P = f"model.layers.{li}.mlp.experts."
+    for e in range(num_experts):
+        g, u = rd.dense64(P + f"{e}.gate_proj"), rd.dense64(P + f"{e}.up_proj")
+        yield torch.cat([g, u], 0).float(), rd.dense64(P + f"{e}.down_proj").float()
+
+
+def write_checkpoint_packs(path: str, cfg, pack_dir: str, layers: Optional[Iterable[int]] = None, **kw) -> list:
+    """Packs for the MoE layers of a checkpoint, coded from its own expert weights."""
+    done = []
+    moe = [li for li in range(cfg.num_layers) if li >= cfg.num_dense_layers]
+    for li in moe:
+        if layers is not None and li not in layers:
+            continue
+        write_layer_pack(pack_dir, li, checkpoint_experts(path, li, cfg.num_experts), **kw)
+        done.append(li)
+    return done
+
+
 def group_pairs(ids: torch.Tensor, rows: int = 8):
     """Decode groups of one step, fixed shapes, on ids' device.
 
