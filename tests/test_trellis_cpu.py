@@ -345,3 +345,12 @@ def test_pack_builder_codes_checkpoint_experts_from_the_source(tmp_path, capsys)
     assert len(eng.generate([[5, 6, 7]], __import__("vllm_moet_b200").SamplingParams(max_tokens=3,
                                                                                  ignore_eos=True))[0]
                .outputs[0].token_ids) == 3
+
+
+def test_trellis_bench_cli_runs_on_cpu(capsys):
+    import json
+    from vllm_moet_b200.utils.trellis_bench import main
+    assert main(["--hidden", "128", "--inter", "64", "--experts", "8", "--top-k", "2", "--tokens", "1,2",
+                 "--iters", "1", "--warmup", "1", "--device", "cpu", "--L", "8"]) == 0
+    recs = [json.loads(x) for x in capsys.readouterr().out.strip().splitlines()]
+    assert [r["tokens"] for r in recs] == [1, 2] and all(r["us_per_block"] > 0 for r in recs)
