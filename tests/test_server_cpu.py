@@ -378,3 +378,19 @@ def test_server_with_prefix_cache_chunked_prefill_and_dspark():
         srv.should_exit = True
         th.join(timeout=10)
         w.close()
+
+
+def test_beam_search_over_http(server):
+    """use_beam_search: the beams come back best first and equal LLM.beam_search."""
+    url, llm = server
+    from vllm_moet_b200 import BeamSearchParams
+    r = requests.post(url + "/v1/completions", json={"prompt": [5, 6, 7, 8], "max_tokens": 4, "n": 2,
+                                                     "use_beam_search": True, "ignore_eos": True}, timeout=300)
+    assert r.ok, r.text
+    ch = r.json()["choices"]
+    want = llm.beam_search([[5, 6, 7, 8]], BeamSearchParams(beam_width=2, max_tokens=4, ignore_eos=True))[0]
+    assert [c["token_ids"] for c in ch] == [s.generated for s in want.sequences]
+    assert ch[0]["cumulative_logprob"] >= ch[1]["cumulative_logprob"]
+    bad = requests.post(url + "/v1/completions", json={"prompt": [5], "use_beam_search": True, "stream": True},
+                        timeout=60)
+    assert bad.status_code == 400

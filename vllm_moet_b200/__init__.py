@@ -6,6 +6,7 @@ __version__ = "0.1.0"
 
 from .config import EngineConfig, ModelConfig, MoetConfig, ParallelConfig, get_preset  # noqa: F401
 from .engine.sampling_params import RequestOutput, SamplingParams  # noqa: F401
+from .engine.beam_search import BeamSearchOutput, BeamSearchParams  # noqa: F401
 
 
 def __getattr__(name):

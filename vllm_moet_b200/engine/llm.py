@@ -489,6 +489,14 @@ class LLM:
         if len(t) + sp.max_tokens + self.k + 1 > self.ecfg.max_model_len:
             raise ValueError(f"prompt ({len(t)}) + max_tokens ({sp.max_tokens}) exceeds max_model_len")
 
+    def beam_search(self, prompts, params):
+        """Beam search (vLLM's ``LLM.beam_search``): ``params`` is a
+        ``BeamSearchParams``; returns one ``BeamSearchOutput`` per prompt with up to
+        ``beam_width`` sequences, best first.  Built on ``generate`` (one batched call per
+        step over every live beam), so it runs on either engine."""
+        from .beam_search import beam_search
+        return beam_search(self, self._normalize(prompts), params)
+
     def generate(self, prompts, sampling_params: Union[SamplingParams, Sequence[SamplingParams], None] = None,
                  use_tqdm: bool = False, callbacks: Optional[Sequence] = None, request_ids: Optional[Sequence] = None,
                  between_steps=None) -> List[RequestOutput]:

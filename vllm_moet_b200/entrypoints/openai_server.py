@@ -410,6 +410,38 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
             return list(p)
         raise HTTPException(400, "prompt must be a string or a list of token ids")
 
+    async def beam_completion(body, params, plist, rid, created):
+        """``use_beam_search``: beam width = ``n`` (or ``best_of``), the search driven through
+        the engine queue -- each step's beams are one-token requests served concurrently."""
+        from ..engine.beam_search import BeamSearchParams, search_steps, step_params
+        if body.get("stream"):
+            raise HTTPException(400, "beam search does not stream")
+        try:
+            bp = BeamSearchParams(beam_width=int(body.get("best_of") or params.n), max_tokens=params.max_tokens,
+                                  ignore_eos=params.ignore_eos, length_penalty=float(body.get("length_penalty", 1.0)))
+        except ValueError as e:
+            raise HTTPException(400, str(e))
+        gen = search_steps(plist, bp, tok.eos_token_id, tok.decode)
+        sp = step_params(bp)
+        try:
+            batch = next(gen)
+            while True:
+                res = await asyncio.gather(*[collect(run_request(b, sp)) for b in batch])
+                batch = gen.send([r[2][0] for r in res])
+        except StopIteration as stop:
+            outs = stop.value
+        choices, n_out = [], 0
+        for j, o in enumerate(outs):
+            for s_ in o.sequences[:params.n]:
+                n_out += len(s_.generated)
+                choices.append({"index": len(choices), "text": s_.text, "token_ids": s_.generated,
+                                "finish_reason": s_.finish_reason, "cumulative_logprob": s_.cum_logprob,
+                                "logprobs": None})
+        return JSONResponse({"id": rid, "object": "text_completion", "created": created, "model": name,
+                             "choices": choices,
+                             "usage": {"prompt_tokens": sum(map(len, plist)), "completion_tokens": n_out,
+                                       "total_tokens": sum(map(len, plist)) + n_out}})
+
     @app.post("/v1/completions")
     async def completions(body: Dict[str, Any]):
         try:
@@ -426,6 +458,8 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
             plist = [_prompt_ids(prompts)]
             raw = [prompts]
         rid, created = f"cmpl-{uuid.uuid4().hex[:24]}", int(time.time())
+        if body.get("use_beam_search"):
+            return await beam_completion(body, params, plist, rid, created)
         if body.get("stream"):
             if len(plist) != 1 or params.n != 1:
                 raise HTTPException(400, "streaming serves one prompt and one completion per request")
