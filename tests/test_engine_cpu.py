@@ -335,3 +335,24 @@ def test_reference_dsa_selection():
     mw.cfg = small
     sparse, _ = reference.forward(mw, toks, torch.arange(T), cs)
     assert not torch.allclose(sparse, dense)
+
+
+def test_allowed_token_ids_match_masked_greedy(tiny_llm):
+    """allowed_token_ids (vLLM's field): greedy decoding over the allowed tokens only, the
+    first token included, equal to a greedy loop over the oracle's masked logits."""
+    allowed = [11, 200, 345, 678, 901]
+    p = [5, 9, 17, 33]
+    got = tiny_llm.generate([p], SamplingParams(max_tokens=5, ignore_eos=True, allowed_token_ids=allowed))
+    got = got[0].outputs[0].token_ids
+    cs = reference.rope_cos_sin(tiny_llm.mw.cfg, 64)
+    seq, want = list(p), []
+    for _ in range(5):
+        lg, _ = reference.forward(tiny_llm.mw, torch.tensor(seq), torch.arange(len(seq)), cs)
+        m = torch.full_like(lg[-1], float("-inf"))
+        m[allowed] = 0
+        t = int(torch.argmax(lg[-1] + m))
+        want.append(t)
+        seq.append(t)
+    assert got == want and set(got) <= set(allowed)
+    with pytest.raises(ValueError):
+        SamplingParams(allowed_token_ids=[])

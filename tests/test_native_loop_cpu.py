@@ -415,3 +415,13 @@ def test_chunked_prefill_in_the_gpu_loop(engine):
     assert sum(1 for c in log if c[3] == 1) >= 5                   # chunks beside the decoding row
     assert llm.runner.chunks == [(s, e) for _, s, e, _ in log[:-1]]
     assert llm.runner.starts_log[-1] == [log[-1][1]]
+
+
+def test_allowed_token_ids_in_the_gpu_loop(engine):
+    """allowed_token_ids on the GPU loop: the row's dense bias keeps only the allowed
+    tokens, so every emitted token is one of them; a greedy row beside it keeps the chain."""
+    llm = engine()
+    only = SamplingParams(max_tokens=6, ignore_eos=True, allowed_token_ids=[77, 78])
+    out = llm.generate([[5, 6, 7], [9, 10]], [SamplingParams(max_tokens=6, ignore_eos=True), only])
+    assert out[0].outputs[0].token_ids == chain([5, 6, 7], 6)
+    assert set(out[1].outputs[0].token_ids) <= {77, 78} and len(out[1].outputs[0].token_ids) == 6

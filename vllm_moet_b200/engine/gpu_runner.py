@@ -1623,6 +1623,9 @@ class DecodeState:
             if b:
                 pr["bias"][row, torch.tensor(list(b), dtype=torch.long).to(dev)] = \
                     torch.tensor(list(b.values()), dtype=torch.float32).to(dev)
+        if params.allowed_token_ids is not None:     # only these tokens: the rest biased out
+            from ..spec.logits_process import allowed_bias
+            pr["bias"][row] += allowed_bias(params.allowed_token_ids, V, dev)
 
     def count_tokens(self, rows, tokens):
         """Generated tokens of the last step (host lists) into the rows' counts."""

@@ -26,6 +26,7 @@ class SamplingParams:
     repetition_penalty: float = 1.0  # tokens of the prompt or the output: positive logits / r, negative * r
     logit_bias: Optional[Dict[int, float]] = None   # token id -> added to its logit
     min_p: float = 0.0              # sampling: drop tokens below min_p x the top token's probability
+    allowed_token_ids: Optional[List[int]] = None   # only these tokens can be chosen (vLLM's field)
 
     def __post_init__(self):
         if isinstance(self.stop, str):
@@ -49,12 +50,16 @@ class SamplingParams:
             raise ValueError("presence_penalty and frequency_penalty must be in [-2, 2]")
         if self.logit_bias:
             self.logit_bias = {int(k): float(v) for k, v in self.logit_bias.items()}
+        if self.allowed_token_ids is not None:
+            self.allowed_token_ids = sorted({int(t) for t in self.allowed_token_ids})
+            if not self.allowed_token_ids:
+                raise ValueError("allowed_token_ids must not be empty")
 
     @property
     def processes_logits(self) -> bool:
         """Whether the logits are changed before choosing a token (penalties, bias)."""
         return bool(self.presence_penalty or self.frequency_penalty or self.repetition_penalty != 1.0
-                    or self.logit_bias)
+                    or self.logit_bias or self.allowed_token_ids is not None)
 
 
 def find_stop(text: str, stops: List[str], start: int = 0):

@@ -180,7 +180,8 @@ def _params_from(body: Dict[str, Any], default_max: int = 16) -> SamplingParams:
                           frequency_penalty=float(body.get("frequency_penalty") or 0.0),
                           repetition_penalty=float(body.get("repetition_penalty") or 1.0),
                           min_p=float(body.get("min_p") or 0.0),
-                          logit_bias={int(k): float(v) for k, v in (body.get("logit_bias") or {}).items()} or None)
+                          logit_bias={int(k): float(v) for k, v in (body.get("logit_bias") or {}).items()} or None,
+                          allowed_token_ids=body.get("allowed_token_ids"))
 
 
 class _ChatParseStream:

@@ -1,6 +1,7 @@
 """Logits processing before a token is chosen: repetition / presence / frequency
-penalties and logit bias, with vLLM's semantics (``SamplingParams`` fields of the same
-names).
+penalties, logit bias and the allowed-token restriction, with vLLM's semantics
+(``SamplingParams`` fields of the same names).  Disallowed tokens get ``DISALLOWED`` added
+(a finite -1e30, so no later arithmetic turns a row into NaN).
 
 Speculative verify: row j of a verify pass scores the token after the pending token and
 drafts ``d_1 .. d_j``.  The drafts before it count as generated text for row j: if row j's
@@ -12,6 +13,16 @@ from __future__ import annotations
 from typing import Optional, Sequence
 
 import torch
+
+DISALLOWED = -1e30
+
+
+def allowed_bias(allowed, V: int, device=None) -> torch.Tensor:
+    """[V] additive bias: 0 for the allowed tokens, DISALLOWED for every other."""
+    b = torch.full((V,), DISALLOWED, dtype=torch.float32, device=device)
+    ids = torch.tensor([t for t in allowed if 0 <= t < V], dtype=torch.long, device=device)
+    b[ids] = 0.0
+    return b
 
 
 def process_logits(logits: torch.Tensor, sp, prompt: Sequence[int], out: Sequence[int],
@@ -41,4 +52,6 @@ def process_logits(logits: torch.Tensor, sp, prompt: Sequence[int], out: Sequenc
         ids = torch.tensor([t for t in sp.logit_bias if 0 <= t < V], dtype=torch.long, device=dev)
         if len(ids):
             x[:, ids] += torch.tensor([sp.logit_bias[int(t)] for t in ids], device=dev)
+    if sp.allowed_token_ids is not None:
+        x = x + allowed_bias(sp.allowed_token_ids, V, dev)[None]
     return x
