@@ -356,3 +356,8 @@ def test_allowed_token_ids_match_masked_greedy(tiny_llm):
     assert got == want and set(got) <= set(allowed)
     with pytest.raises(ValueError):
         SamplingParams(allowed_token_ids=[])
+
+
+def test_get_tokenizer(tiny_llm):
+    tok = tiny_llm.get_tokenizer()
+    assert tok is tiny_llm.tokenizer and tok.decode(tok.encode("ab")) == "ab"

@@ -489,6 +489,10 @@ class LLM:
         if len(t) + sp.max_tokens + self.k + 1 > self.ecfg.max_model_len:
             raise ValueError(f"prompt ({len(t)}) + max_tokens ({sp.max_tokens}) exceeds max_model_len")
 
+    def get_tokenizer(self):
+        """The engine's tokenizer (vLLM's ``LLM.get_tokenizer``)."""
+        return self.tokenizer
+
     def beam_search(self, prompts, params):
         """Beam search (vLLM's ``LLM.beam_search``): ``params`` is a
         ``BeamSearchParams``; returns one ``BeamSearchOutput`` per prompt with up to
