@@ -83,3 +83,28 @@ def test_wire_format_roundtrip():
     finally:
         a.close()
         b.close()
+
+
+def test_chain_with_trellis_served_experts(tmp_path):
+    """Each stage serves its MoE layers from the trellis packs (global layer ids); the chain
+    equals the single-process oracle under the same tier."""
+    from vllm_moet_b200.residency import trellis_tier as tt
+    cfg = _cfg()
+    full = random_weights(cfg, "cpu", seed=0, with_mtp=False)
+    layers = tt.write_model_packs(full, str(tmp_path), L=6)
+    tier = tt.TrellisBaseTier(str(tmp_path), layers, act_limit=cfg.swiglu_limit)
+    prompt = [5, 9, 17, 33, 65, 129]
+    with reference.moe_context(tier.moe_fn(full)):
+        want = reference.greedy_generate(full, prompt, 5)
+    ls = socket.create_server(("127.0.0.1", 0))
+    th = threading.Thread(target=serve_stage, args=(Stage(cfg, 1, 2, trellis_pack=str(tmp_path)), ls, None, 0.0),
+                          daemon=True)
+    th.start()
+    d = Driver(Stage(cfg, 0, 2, trellis_pack=str(tmp_path)), ("127.0.0.1", ls.getsockname()[1]))
+    try:
+        assert d.st.moe_fn is not None
+        assert d.generate(prompt, 5)["tokens"] == want
+    finally:
+        d.close()
+        th.join(timeout=30)
+        ls.close()

@@ -8,7 +8,8 @@ no CUDA graph and no speculation.  Per generated token the driver reports
 replies) and ``link`` (the rest of the round trip), which is the term the
 prototype exists to validate.  Reference: ``tools/pp_proto_exl3.py`` (patch
 P:1491-1735) -- there two stages of DS4-Flash with EXL3-served experts; here
-any number of stages of any preset, experts from the 2-bit planes.
+any number of stages of any preset, experts from the 2-bit planes or, with
+``--trellis-pack``, from the trellis (EXL3-style) base tier.
 
 Wire format (no pickle: a peer's bytes are never executed): one frame is
 ``u64 total | u32 header bytes | JSON header | tensor bytes``; the header lists
@@ -98,11 +99,20 @@ class Stage:
     """Layers [lo, hi) of a `stages`-way split (the engine's PP layer ranges)."""
 
     def __init__(self, cfg: ModelConfig, stage: int, stages: int, device="cpu", seed: int = 0,
-                 max_pos: int = 4096):
+                 max_pos: int = 4096, trellis_pack: Optional[str] = None):
         self.cfg, self.stage, self.stages = cfg, stage, stages
         self.dev = torch.device(device)
         self.mw = random_weights(cfg, self.dev, seed=seed, with_mtp=False, pp_rank=stage, pp_size=stages)
         self.lo, self.hi = self.mw.extra["layer_range"]
+        self.moe_fn = None
+        if trellis_pack:            # this stage's MoE layers from the trellis packs (global layer ids)
+            import os
+            from ..residency.trellis_tier import TrellisBaseTier, pack_path
+            mine = [self.lo + i for i, lw in enumerate(self.mw.layers)
+                    if lw.is_moe and os.path.exists(pack_path(trellis_pack, self.lo + i))]
+            if mine:
+                tier = TrellisBaseTier(trellis_pack, mine, device=self.dev, act_limit=cfg.swiglu_limit)
+                self.moe_fn = tier.moe_fn(self.mw, layer_offset=self.lo)
         self.first, self.last = stage == 0, stage == stages - 1
         self.cs = ref.rope_cos_sin(cfg, max_pos, self.dev)
         self.reset()
@@ -118,8 +128,10 @@ class Stage:
         if self.first and self.cfg.hc_mult > 1:           # hyper-connections: [T, n, H] streams on the wire
             h = h[:, None, :].expand(-1, self.cfg.hc_mult, -1)
         pos = positions.to(self.dev)
-        for i, lw in enumerate(self.mw.layers):
-            h = ref.decoder_layer(self.cfg, lw, h, pos, self.cs, self.cache, i)
+        import contextlib
+        with ref.moe_context(self.moe_fn) if self.moe_fn is not None else contextlib.nullcontext():
+            for i, lw in enumerate(self.mw.layers):
+                h = ref.decoder_layer(self.cfg, lw, h, pos, self.cs, self.cache, i)
         return h.to(torch.bfloat16)
 
     @torch.inference_mode()
@@ -236,13 +248,14 @@ def main(argv=None):
     ap.add_argument("--rtt-ms", type=float, default=0.0)
     ap.add_argument("--prompt-len", type=int, default=32)
     ap.add_argument("--new-tokens", type=int, default=16)
+    ap.add_argument("--trellis-pack", default=None, help="serve the routed experts from these trellis packs")
     args = ap.parse_args(argv)
     cfg = get_preset(args.model)
     if args.num_layers:
         cfg = cfg.replace(num_layers=args.num_layers)
     if args.hc_mult:
         cfg = cfg.replace(hc_mult=args.hc_mult)
-    st = Stage(cfg, args.stage, args.stages, args.device)
+    st = Stage(cfg, args.stage, args.stages, args.device, trellis_pack=args.trellis_pack)
     if args.stage > 0:
         ls = socket.create_server(("0.0.0.0", args.port))
         nxt = None

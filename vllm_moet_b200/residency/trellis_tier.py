@@ -299,11 +299,12 @@ class TrellisBaseTier:
         y = sum(proj(pl, h, own, "w2", wp if pl[4] is None else wp * pl[4]) for pl in plans)
         return y.view(T, k, self.H).sum(1)              # fixed order over k: deterministic
 
-    def moe_fn(self, mw):
+    def moe_fn(self, mw, layer_offset: int = 0):
         """A ``reference.moe_context`` function: routed experts from this tier for its
-        layers (the model's own experts elsewhere), plus the shared expert."""
+        layers (the model's own experts elsewhere), plus the shared expert.
+        ``layer_offset``: the global index of ``mw.layers[0]`` (a pipeline stage's range)."""
         from ..models import reference as ref
-        index = {id(lw): li for li, lw in enumerate(mw.layers)}
+        index = {id(lw): li + layer_offset for li, lw in enumerate(mw.layers)}
         if self.act_limit is None:
             self.act_limit = mw.cfg.swiglu_limit
 
