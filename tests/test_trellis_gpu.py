@@ -107,3 +107,40 @@ def test_trellis_delta_pool_gpu_matches_cpu(tmp_path):
         got = tiers["cuda"][0].forward_topk(0, x.cuda(), ids.cuda(), w.cuda(), delta=tiers["cuda"][1])
         torch.cuda.synchronize()
         assert _rel(got, want) < 1e-4, T
+
+
+def test_gpu_engine_serves_the_trellis_tier(tmp_path):
+    """The GPU engine with trellis packs: its prefill logits track the fp32 oracle whose MoE
+    blocks run through the same tier (routing, per-pair outputs, weighted combine with the
+    residual and the shared expert), and graph-replayed decode is deterministic."""
+    from vllm_moet_b200 import SamplingParams
+    from vllm_moet_b200.config import ds4_flash_config
+    from vllm_moet_b200.engine.llm import LLM
+    from vllm_moet_b200.models import reference
+    cfg = ds4_flash_config(num_layers=2, hidden=1024, vocab=2048, num_experts=8, moe_intermediate=128,
+                           dense_intermediate=512, num_heads=8, q_lora_rank=256, top_k=2)
+    base = LLM(cfg, device="cuda", num_speculative_tokens=0, max_model_len=512, max_num_seqs=2, seed=0)
+    layers = tt.write_model_packs(base.mw, str(tmp_path), L=8, device=torch.device("cuda"))
+    del base
+    torch.cuda.empty_cache()
+    llm = LLM(cfg, device="cuda", num_speculative_tokens=0, max_model_len=512, max_num_seqs=2, seed=0,
+              trellis_pack=str(tmp_path))
+    assert llm.trellis is not None and sorted(llm.trellis.layers) == layers and llm.runner.trellis is llm.trellis
+    g = torch.Generator().manual_seed(21)
+    p = torch.randint(3, 2048, (40,), generator=g).tolist()
+    st = llm._state(1)
+    blocks = llm.blocks.allocate("tr", 128)
+    bt = torch.zeros(1, llm.max_blocks, dtype=torch.int32)
+    bt[0, :len(blocks)] = torch.tensor(blocks)
+    st.block_table.copy_(bt)
+    llm.runner.prefill([p], [bt[0].tolist()], [0], st)
+    lg = llm.runner.ws_prefill.bufs[("main.logits", torch.float32)].reshape(-1, cfg.vocab)[-1].clone()
+    llm.blocks.release("tr")
+    cs = reference.rope_cos_sin(llm.cfg, 256, "cuda")
+    with reference.moe_context(llm.trellis.moe_fn(llm.mw)):
+        want, _ = reference.forward(llm.mw, torch.tensor(p, device="cuda"), torch.arange(len(p), device="cuda"), cs)
+    assert _rel(lg, want[-1]) < 0.1
+    sp = SamplingParams(max_tokens=8, ignore_eos=True)
+    a = [o.outputs[0].token_ids for o in llm.generate([p, p[:17]], sp)]
+    b = [o.outputs[0].token_ids for o in llm.generate([p, p[:17]], sp)]
+    assert a == b and all(len(x) == 8 for x in a)

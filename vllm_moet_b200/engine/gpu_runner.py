@@ -167,6 +167,9 @@ class NativeRunner:
         self.delta = None         # residency.DeltaTier (FP4 hot experts) when enabled
         self._moe_index = {}
         self._looka = None        # router lookahead (enable_looka)
+        self.trellis = None       # residency.TrellisBaseTier serving the routed experts of its layers
+        self.trellis_delta = None
+        self._trellis_li = {}
         self._route_tag = ""      # routing-buffer suffix of the current MTP draft pass
         self._pend = None         # (residual, out) of a pushed reduction the next RMSNorm completes
         self._pend_add = None     # (residual, reduced partial, out): decode residual add left to the next norm
@@ -534,6 +537,14 @@ class NativeRunner:
             if self.pilot_log is not None:
                 self.pilot_log[mli + 1, :T].copy_(pid)
 
+    def attach_trellis(self, tier, delta=None):
+        """Serve the routed experts of the tier's layers from trellis-coded weights (one rank,
+        no expert cache / delta tier): the router as usual, then the tier's rotation +
+        trellis-decode kernels per routing pair, then the usual expert combine.  Fixed shapes
+        and no host synchronisation, so the step stays capturable."""
+        self.trellis, self.trellis_delta = tier, delta
+        self._trellis_li = {id(lw): li for li, lw in enumerate(self.mw.layers) if li in tier.layers}
+
     def attach_delta_tier(self, tier):
         """Serve experts that hold a delta slot at FP4 precision (decode GEMVs)."""
         from ..residency import moe_layers
@@ -859,7 +870,8 @@ class NativeRunner:
             else:
                 C.moe_combine(yk, none, wts, rx, sh, out, None)
             return
-        if T <= 64 and not use_tc and H % 1024 == 0 and topp <= 0:
+        tl = self._trellis_li.get(id(lw)) if self.trellis is not None else None
+        if T <= 64 and not use_tc and H % 1024 == 0 and topp <= 0 and tl is None:
             # decode: logits + top-k + pair list in one launch
             MB = ctx.mb
             P = R // MB + min(E_loc, R)
@@ -887,7 +899,10 @@ class NativeRunner:
                 wts.copy_(pw)
             self._looka_step(mli, hb, ids, ctx)
             self._ensure_experts(mli, ids)
-            if use_tc:
+            if tl is not None:      # trellis base tier: per-pair outputs, combined below
+                y2 = self.trellis.forward_pairs(tl, hb, ids, delta=self.trellis_delta)
+                posof = self.ws.get("trellis.nopos", (0,), torch.int32)
+            elif use_tc:
                 y2, posof = self._moe_tc(h2q, h2s, ids, ex, R, T, E_loc, e_lo)
             elif (self.decode_tc_nt and ctx.mode == "decode" and H % 128 == 0 and I % 128 == 0
                   and self.delta is None):

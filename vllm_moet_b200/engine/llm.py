@@ -85,9 +85,6 @@ class LLM:
         self._dcp = None
         if self.device.type == "cuda" and sp_group is not None and (enable_prefix_caching or enable_chunked_prefill):
             raise NotImplementedError("GPU SP prefill: no prefix caching or chunked prefill")
-        if self.device.type == "cuda" and (trellis_pack or os.environ.get("VLLM_MOE_W2_EXL3_PACK")):
-            raise NotImplementedError("trellis base tier: served by the CPU engine; on a GPU its kernels run through "
-                                      "residency.trellis_tier.TrellisBaseTier.forward_topk")
         self._sp_group = sp_group
         self._ep_group = ep_group
         if speculative_method not in ("mtp", "dspark", "dflash", "eagle3"):
@@ -240,6 +237,12 @@ class LLM:
             self.delta = self.gate = None
             if delta_slots:
                 self._attach_delta(delta_slots, gate)
+            trellis_pack = trellis_pack or os.environ.get("VLLM_MOE_W2_EXL3_PACK") or None
+            self.trellis = None
+            if trellis_pack:
+                if slots or delta_slots:
+                    raise NotImplementedError("trellis base tier: not with an expert cache or an FP4 delta tier")
+                self.trellis = self._attach_trellis(trellis_pack, tp_group, pp_group, sp_group, dcp_group, ep_group)
             self._attach_tracing()
             self._DecodeState = DecodeState
             self._states = {}
@@ -263,7 +266,8 @@ class LLM:
 
     def _attach_trellis(self, pack_dir, *groups):
         """Serve the routed experts of every MoE layer that has a pack in ``pack_dir`` from
-        the trellis base tier (single rank, unsharded experts)."""
+        the trellis base tier (single rank, unsharded experts): on the CPU engine through
+        the oracle's MoE hook, on the GPU inside the runner's MoE step."""
         from ..residency.trellis_tier import TrellisBaseTier, pack_path
         if any(g is not None for g in groups):
             raise NotImplementedError("trellis base tier: one rank with every expert (no TP / PP / SP / DCP / EP)")
@@ -271,7 +275,10 @@ class LLM:
         if not layers:
             raise FileNotFoundError(f"no trellis packs (exl3-lNN.safetensors) for the MoE layers in {pack_dir}")
         tier = TrellisBaseTier(pack_dir, layers, device=self.device, act_limit=self.mw.cfg.swiglu_limit)
-        self.runner.moe_impl = tier.moe_fn(self.mw)
+        if self.device.type == "cuda":
+            self.runner.attach_trellis(tier)       # inside the GPU runner's MoE step (capturable)
+        else:
+            self.runner.moe_impl = tier.moe_fn(self.mw)
         return tier
 
     def _attach_tracing(self):

@@ -125,15 +125,17 @@ def _check(K: int, L: int):
 def codes_to_words(codes: torch.Tensor, K: int) -> torch.Tensor:
     """codes [B, 256] (K-bit ints) -> words [B, 16K] int16 (MSB-first stream)."""
     B = codes.shape[0]
-    bits = ((codes.to(torch.int64)[..., None] >> torch.arange(K - 1, -1, -1)) & 1).reshape(B, 256 * K)
-    w = (bits.view(B, 16 * K, 16) << torch.arange(15, -1, -1)).sum(-1)
+    dev = codes.device
+    bits = ((codes.to(torch.int64)[..., None] >> torch.arange(K - 1, -1, -1, device=dev)) & 1).reshape(B, 256 * K)
+    w = (bits.view(B, 16 * K, 16) << torch.arange(15, -1, -1, device=dev)).sum(-1)
     return w.to(torch.int32).to(torch.int16)
 
 
 def words_to_bits(words: torch.Tensor) -> torch.Tensor:
     """words [..., n] int16 -> bits [..., 16 n] (0/1 int64), MSB of word 0 first."""
     w = words.to(torch.int64) & 0xFFFF
-    return ((w[..., None] >> torch.arange(15, -1, -1)) & 1).reshape(*words.shape[:-1], words.shape[-1] * 16)
+    sh = torch.arange(15, -1, -1, device=words.device)
+    return ((w[..., None] >> sh) & 1).reshape(*words.shape[:-1], words.shape[-1] * 16)
 
 
 @functools.lru_cache(maxsize=None)
@@ -147,13 +149,13 @@ def _window_index(K: int, L: int) -> torch.Tensor:
 def tile_states(words: torch.Tensor, K: int, L: int) -> torch.Tensor:
     """words [..., 16K] -> the 256 trellis states of each tile [..., 256]."""
     bits = words_to_bits(words)
-    win = bits[..., _window_index(K, L)]                      # [..., 256, L]
-    return (win << torch.arange(L - 1, -1, -1)).sum(-1)
+    win = bits[..., _window_index(K, L).to(words.device)]     # [..., 256, L]
+    return (win << torch.arange(L - 1, -1, -1, device=words.device)).sum(-1)
 
 
 def decode_tiles(words: torch.Tensor, K: int, L: int, codebook: str = "3inst") -> torch.Tensor:
     """words [..., 16K] -> normalised tile values [..., 256] fp32."""
-    return codebook_table(L, codebook)[tile_states(words, K, L)]
+    return codebook_table(L, codebook).to(words.device)[tile_states(words, K, L)]
 
 
 # ---------------------------------------------------------------- Viterbi encoder
@@ -242,7 +244,8 @@ def quantize_linear(w: torch.Tensor, K: int, L: int = 16, codebook: str = "3inst
     if Kin % TILE or N % TILE:
         raise ValueError(f"trellis tiles need both dims divisible by {TILE}, got {tuple(w.shape)}")
     gen = torch.Generator().manual_seed(seed)
-    wt = w.double().t()                                            # [Kin, N]
+    dev = device if device is not None else w.device
+    wt = w.detach().double().cpu().t()                             # [Kin, N]
     col = wt.pow(2).mean(0).sqrt()
     sv = (_signs(N, gen) * torch.where(col > 0, col, torch.ones_like(col))).half()
     wt = wt / sv.double()[None, :]
@@ -251,7 +254,6 @@ def quantize_linear(w: torch.Tensor, K: int, L: int = 16, codebook: str = "3inst
     wt = wt / su.double()[:, None]
     Qm = fwht(fwht(wt.t()).t())                                    # Hk · wt · Hn
     tiles = _tiles_of(Qm.float())
-    dev = device if device is not None else w.device
     words = encode_tiles(tiles.reshape(-1, 256).to(dev), K, L, codebook).cpu()
     return {"trellis": words.reshape(Kin // TILE, N // TILE, 16 * K), "suh": su, "svh": sv}
 

@@ -259,6 +259,17 @@ class TrellisBaseTier:
             out.index_add_(0, rows.cpu(), y * w[rows, slot, None].cpu())
         return out.to(x.device)
 
+    @torch.no_grad()
+    def forward_pairs(self, li: int, x: torch.Tensor, ids: torch.Tensor,
+                      delta: Optional["TrellisDeltaPool"] = None) -> torch.Tensor:
+        """Per routing pair, unweighted: [T·k, H] fp32, row t·k + j = expert ids[t, j] on
+        x[t] (base + delta for pooled experts).  The GPU engine's expert combine applies the
+        routing weights, the residual and the shared expert.  CUDA tensors only."""
+        streams = [self._stream(li)]
+        if delta is not None and li in delta.layers:
+            streams.append(delta._stream(li))
+        return self._forward_native(x, ids, None, streams)
+
     def _forward_native(self, x, ids, w, streams):
         from ..ops import native
         C = native()
@@ -268,7 +279,7 @@ class TrellisBaseTier:
         xf = x.float().contiguous()
         src = torch.arange(P, device=dev, dtype=torch.int32) // k
         own = torch.arange(P, device=dev, dtype=torch.int32)
-        wp = w.reshape(P).contiguous()
+        wp = w.reshape(P).contiguous() if w is not None else None
         plans = []
         for sm in streams:
             if sm["slot_of"] is None:     # base: every pair, groups of distinct experts per token
@@ -296,6 +307,8 @@ class TrellisBaseTier:
         g = sum(proj(pl, xf, src, "w1", pl[4]) for pl in plans)
         u = sum(proj(pl, xf, src, "w3", pl[4]) for pl in plans)
         h = self._swiglu(g, u).contiguous()
+        if wp is None:                                  # per pair, unweighted
+            return sum(proj(pl, h, own, "w2", pl[4]) for pl in plans)
         y = sum(proj(pl, h, own, "w2", wp if pl[4] is None else wp * pl[4]) for pl in plans)
         return y.view(T, k, self.H).sum(1)              # fixed order over k: deterministic
 
