@@ -285,7 +285,7 @@ class TrellisBaseTier:
             if sm["slot_of"] is None:     # base: every pair, groups of distinct experts per token
                 rid, sel, maxr = ids, None, min(T, 8)
             else:                         # delta: pooled pairs; the others read slot 0, weighted 0
-                so = sm["slot_of"].to(dev)[ids.long()]
+                so = sm["slot_dev"][ids.long()]      # device tensor: no copy inside a captured step
                 sel = (so >= 0).float().reshape(P).contiguous()
                 rid, maxr = so.clamp_min(0), 8
             experts, row_map = group_pairs(rid)
@@ -368,6 +368,7 @@ class TrellisDeltaPool:
         H, I, dev = tier.H, tier.I, tier.dev
         self.layers: Dict[int, Dict[str, torch.Tensor]] = {}
         self.slot_of: Dict[int, torch.Tensor] = {}
+        self.slot_dev: Dict[int, torch.Tensor] = {}
         self.order: Dict[int, list] = {}
         self._q: Dict[tuple, torch.Tensor] = {}
         for li in (layers if layers is not None else tier.layers):
@@ -379,12 +380,14 @@ class TrellisDeltaPool:
                 st[f"{name}.svh"] = torch.zeros(self.slots, n, dtype=torch.float16, device=dev)
             self.layers[li] = st
             self.slot_of[li] = torch.full((tier.E,), -1, dtype=torch.int32)
+            self.slot_dev[li] = self.slot_of[li].to(dev)     # the device copy the kernels' step reads
             self.order[li] = []
         self.stats = {"promoted": 0, "evicted": 0}
 
     def _stream(self, li: int) -> dict:
         return dict(st=self.layers[li], K13=self.dk13, K2=self.dk2, L=self.L, codebook=self.codebook,
-                    inv_rms=self.inv_rms, slot_of=self.slot_of[li], qcache=self._q, key=("delta", li))
+                    inv_rms=self.inv_rms, slot_of=self.slot_of[li], slot_dev=self.slot_dev[li], qcache=self._q,
+                    key=("delta", li))
 
     def promote(self, li: int, e: int, w13: torch.Tensor, w2: torch.Tensor, device=None) -> int:
         """Code expert e's residual against the base tier into a slot; returns the slot.
@@ -417,6 +420,7 @@ class TrellisDeltaPool:
             for key in [k_ for k_ in self._q if k_[:2] == ("delta", li) and k_[2] == s]:
                 del self._q[key]
         so[e] = s
+        self.slot_dev[li].copy_(so)
         self.order[li].append(e)
         self.stats["promoted"] += 1
         return s
@@ -425,6 +429,7 @@ class TrellisDeltaPool:
         so = self.slot_of[li]
         if int(so[e]) >= 0:
             so[e] = -1
+            self.slot_dev[li].copy_(so)
             self.order[li].remove(e)
             self.stats["evicted"] += 1
 
