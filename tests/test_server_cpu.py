@@ -394,3 +394,13 @@ def test_beam_search_over_http(server):
     bad = requests.post(url + "/v1/completions", json={"prompt": [5], "use_beam_search": True, "stream": True},
                         timeout=60)
     assert bad.status_code == 400
+
+
+def test_constrained_decoding_requests_are_refused(server):
+    url, _ = server
+    for extra in ({"response_format": {"type": "json_object"}}, {"guided_json": {"type": "object"}}):
+        r = requests.post(url + "/v1/completions", json={"prompt": [5, 6], "max_tokens": 2, **extra}, timeout=60)
+        assert r.status_code == 400, (extra, r.text)
+    ok = requests.post(url + "/v1/completions", json={"prompt": [5, 6], "max_tokens": 2,
+                                                      "response_format": {"type": "text"}}, timeout=120)
+    assert ok.ok

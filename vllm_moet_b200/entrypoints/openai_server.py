@@ -157,7 +157,17 @@ def follower_loop(llm, tp_group):
         llm.generate(prompts, params, request_ids=rids, between_steps=between)
 
 
+UNSUPPORTED_FIELDS = ("guided_json", "guided_regex", "guided_choice", "guided_grammar", "structured_outputs")
+
+
 def _params_from(body: Dict[str, Any], default_max: int = 16) -> SamplingParams:
+    # constrained decoding is not served: refuse it instead of answering unconstrained
+    rf = body.get("response_format")
+    if isinstance(rf, dict) and rf.get("type", "text") != "text":
+        raise ValueError(f"response_format {rf.get('type')!r} is not supported (plain text only)")
+    bad = [k for k in UNSUPPORTED_FIELDS if body.get(k) is not None]
+    if bad:
+        raise ValueError(f"constrained decoding is not supported: {', '.join(bad)}")
     temp = float(body.get("temperature", 0.0) or 0.0)
     if temp < 0:
         raise ValueError("temperature must be >= 0")
