@@ -301,6 +301,9 @@ def test_base_cache_misses_are_fetched_and_replayed(engine):
     assert [o.outputs[0].token_ids for o in out] == [chain([5, 6, 7], 9), chain([9, 9], 9)]
     assert llm.replay.stats["replayed_steps"] > 0 and cache.stats["fetched_rows"] > 0
     assert llm.kpi.snapshot()["replayed_steps"] == llm.replay.stats["replayed_steps"]
+    snap = llm.kpi.snapshot()
+    assert snap["pool_slots"] == 10 and abs(snap["pool_pct"] - 62.5) < 1e-9   # 10 of 2 x 8 experts
+    assert "pool 10 slots = 62.5% of experts" in llm.kpi.line()
 
 
 def test_spec_guard_and_draft_affinity_on_the_cache_loop(engine):

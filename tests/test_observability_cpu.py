@@ -17,6 +17,13 @@ def test_kpi_line_and_dump(tmp_path):
     d = json.loads((tmp_path / "kpi.json").read_text())
     assert d["steps"] == 2 and d["read_us"]["p99"] == 300.0
     assert percentiles([1, 2, 3, 4])["p50"] in (2, 3)
+    k.gauge(pool_slots=40, pool_pct=12.5, replay_ema=3.25, looka={"previous_step": 0.5, "router_lookahead": 0.75})
+    k.c["draft_prefetched"] += 7
+    ln = k.line()
+    assert ln.endswith("; pool 40 slots = 12.5% of experts; draft-prefetched 7; replay EMA 3.2%; "
+                       "LOOKA recall prev/router 0.50/0.75") or ln.endswith(
+        "; pool 40 slots = 12.5% of experts; draft-prefetched 7; replay EMA 3.3%; LOOKA recall prev/router 0.50/0.75")
+    assert k.snapshot()["pool_slots"] == 40
 
 
 def test_routing_capture_and_precision_map(tmp_path):

@@ -281,6 +281,17 @@ class LLM:
             self.runner.moe_impl = tier.moe_fn(self.mw)
         return tier
 
+    def _kpi_gauges(self, runner):
+        """The KPI line's latest-value fields (cheap host reads; the LOOKA recall reads two
+        small device counters, so only on the steps the line is printed)."""
+        c = self.cache
+        g = dict(pool_slots=c.n_slots, pool_pct=100.0 * c.n_slots / max(1, c.L * c.E))
+        if self.spec_guard is not None:
+            g["replay_ema"] = 100.0 * float(self.spec_guard.ema)
+        if getattr(runner, "_looka", None) is not None and (self.kpi.steps + 1) % self.kpi.every == 0:
+            g["looka"] = runner.looka_recall()
+        self.kpi.gauge(**g)
+
     def _attach_tracing(self):
         """Prefill span timers, routing capture, delta trace / dump and the gate JSONL
         (reference env names: VLLM_PREFILL_TIMERS_FLUSH, VLLM_MOE_W2_DELTA_TRACE / _DUMP /
@@ -857,7 +868,9 @@ class LLM:
                     # next step's drafts routed to before (asynchronously, off the decode stream)
                     self.affinity.record(snap[0].reshape(-1).tolist(),
                                          [t if t is not None and t.dim() == 2 else None for t in runner.route_ids(B)])
-                    self.affinity.prefetch(st.tokens[:, 1:].reshape(-1).tolist())
+                    n_pf = self.affinity.prefetch(st.tokens[:, 1:].reshape(-1).tolist())
+                    self.kpi.c["draft_prefetched"] += n_pf
+                self._kpi_gauges(runner)
             elif graph is not None:
                 graph.replay()
             else:

@@ -40,6 +40,7 @@ class KpiLogger:
         self.steps = 0
         self.c = collections.Counter()
         self.read_lat_us: collections.deque = collections.deque(maxlen=4096)
+        self.gauges: Dict[str, object] = {}     # latest values (not summed): pool share, EMAs, recalls
 
     def step(self, replayed: bool = False, misses: int = 0, gate_fired: bool = False, **extra):
         self.steps += 1
@@ -51,6 +52,12 @@ class KpiLogger:
         if self.steps % self.every == 0:
             self.flush()
 
+    def gauge(self, **kv):
+        """Latest-value fields of the line: ``pool_slots`` / ``pool_pct`` (cache slots, share of
+        all experts), ``replay_ema`` (the spec guard's EMA, percent), ``looka`` ({previous_step,
+        router_lookahead} recall)."""
+        self.gauges.update(kv)
+
     def record_read(self, us: float):
         self.read_lat_us.append(us)
 
@@ -59,13 +66,31 @@ class KpiLogger:
         d["steps"] = self.steps
         d["replay_pct"] = 100.0 * self.c["replayed_steps"] / max(1, self.steps)
         d["read_us"] = percentiles(list(self.read_lat_us))
+        d.update(self.gauges)
         return d
 
     def line(self) -> str:
         d = self.snapshot()
         return (f"[moet] KPI: steps {d['steps']} replay {d['replay_pct']:.1f}% misses {d['misses']} "
                 f"fetched {d.get('fetched_rows', 0)} rows ({d.get('fetched_bytes', 0) / 2**20:.1f} MiB) "
-                f"gate fires {d['gate_fires']} read p50/p99 {d['read_us']['p50']:.0f}/{d['read_us']['p99']:.0f} us")
+                f"gate fires {d['gate_fires']} read p50/p99 {d['read_us']['p50']:.0f}/{d['read_us']['p99']:.0f} us"
+                + self._tail(d))
+
+    @staticmethod
+    def _tail(d: dict) -> str:
+        """The optional fields, in the reference's KPI order: pool share, draft-prefetched
+        experts, replay EMA, LOOKA recall."""
+        out = []
+        if "pool_slots" in d:
+            out.append(f"pool {d['pool_slots']} slots = {d.get('pool_pct', 0.0):.1f}% of experts")
+        if d.get("draft_prefetched"):
+            out.append(f"draft-prefetched {d['draft_prefetched']}")
+        if "replay_ema" in d:
+            out.append(f"replay EMA {d['replay_ema']:.1f}%")
+        if "looka" in d:
+            lk = d["looka"]
+            out.append(f"LOOKA recall prev/router {lk.get('previous_step', 0.0):.2f}/{lk.get('router_lookahead', 0.0):.2f}")
+        return "".join("; " + x for x in out)
 
     def flush(self):
         self.sink(self.line())
