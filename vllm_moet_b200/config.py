@@ -222,6 +222,10 @@ class MoetConfig:
     gate_agg: str = "min"               # min | q<frac>
     gate_fp_max: int = 3
     gate_max_promote: int = 64
+    # runtime-tunable knobs: a one-line file re-read when it changes (path or None)
+    gate_tau_file: Optional[str] = None
+    gate_max_promote_file: Optional[str] = None
+    base_miss_tol_file: Optional[str] = None
     # stores
     store_dir: Optional[str] = None
     base_ram_gb: Optional[str] = None
@@ -268,6 +272,9 @@ class MoetConfig:
         "delta_decay": "VLLM_MOE_W2_DELTA_DECAY",
         "base_cache_gb": "VLLM_MOE_W2_BASE_CACHE_GB",
         "base_miss_tol": "VLLM_MOE_W2_BASE_MISS_TOL",
+        "base_miss_tol_file": "VLLM_MOE_W2_BASE_MISS_TOL_FILE",
+        "gate_tau_file": "VLLM_MOE_W2_GATE_TAU_FILE",
+        "gate_max_promote_file": "VLLM_MOE_W2_GATE_MAX_PROMOTE_FILE",
         "fp_max": "VLLM_MOE_W2_FP_MAX",
         "replay_mode": "VLLM_MOE_W2_REPLAY_MODE",
         "kpi_every": "VLLM_MOE_W2_KPI_EVERY",

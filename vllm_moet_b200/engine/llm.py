@@ -381,7 +381,8 @@ class LLM:
         self.runner.attach_delta_tier(self.delta)
         if gate if gate is not None else m.gate:
             self.gate = ConfidenceGate(tau=m.gate_tau, signal=m.gate_signal, agg=m.gate_agg, fp_max=m.gate_fp_max,
-                                       max_promote=m.gate_max_promote)
+                                       max_promote=m.gate_max_promote, tau_file=m.gate_tau_file,
+                                       max_promote_file=m.gate_max_promote_file)
             self.ecfg.cuda_graphs = self.ecfg.cuda_graphs  # gate replays reuse the captured graph
 
     def _routed_pairs(self, B):
@@ -430,7 +431,7 @@ class LLM:
         self.runner.attach_expert_cache(self.cache)
         self.replay = ReplayEngine(self.cache, tp_group=tp_group, pp_group=self._pp_group, mode=m.replay_mode,
                                    fp_max=m.fp_max,
-                                   miss_tol=m.base_miss_tol)
+                                   miss_tol=m.base_miss_tol, miss_tol_file=m.base_miss_tol_file)
         self.affinity = DraftAffinity(self.cache) if m.prefetch and self.k > 0 else None
         self.pilot = None
         if m.looka or m.pilot:

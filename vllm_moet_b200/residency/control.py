@@ -50,14 +50,27 @@ class ReplayEngine:
     bitmap stays per stage (reference: PP base segment replay, M5 / M9)."""
 
     def __init__(self, cache: ExpertCache, tp_group=None, mode: str = "strict", fp_max: int = 32,
-                 miss_tol: int = 0, comm_device=None, pp_group=None):
+                 miss_tol: int = 0, comm_device=None, pp_group=None, miss_tol_file: Optional[str] = None):
         if mode not in ("strict", "approximate"):
             raise ValueError(mode)
+        from ..utils.tunable import tunable
         self.pp_group = pp_group
         self.cache, self.group, self.mode = cache, tp_group, mode
-        self.fp_max, self.miss_tol = fp_max, miss_tol
+        self.fp_max = fp_max
+        # runtime-tunable from a file (BASE_MISS_TOL_FILE); the accept decision is reduced
+        # across the ranks, so ranks that read a new value one step apart still agree
+        self._miss_tol = tunable(miss_tol, miss_tol_file, int, check=lambda v: v >= 0)
         self.comm_device = comm_device or cache.dev
         self.stats = collections.Counter()
+
+    @property
+    def miss_tol(self) -> int:
+        from ..utils.tunable import resolve
+        return resolve(self._miss_tol)
+
+    @miss_tol.setter
+    def miss_tol(self, v: int) -> None:      # a fixed value (replaces a file-backed one)
+        self._miss_tol = v
 
     def missing_pairs(self, route_ids: Sequence[Optional[torch.Tensor]]) -> List[Tuple[int, int]]:
         """route_ids[li]: int tensor of routed expert ids of layer li this step (any shape)."""
@@ -126,10 +139,32 @@ class ReplayEngine:
 
 class ConfidenceGate:
     def __init__(self, tau: float = 0.6, signal: str = "maxprob", agg: str = "min", fp_max: int = 3,
-                 max_promote: int = 64):
-        self.tau, self.signal, self.agg = tau, signal, agg
-        self.fp_max, self.max_promote = fp_max, max_promote
+                 max_promote: int = 64, tau_file: Optional[str] = None, max_promote_file: Optional[str] = None):
+        from ..utils.tunable import tunable
+        # tau and max_promote are runtime-tunable from files (GATE_TAU_FILE / _MAX_PROMOTE_FILE)
+        self._tau = tunable(tau, tau_file, float, check=lambda v: 0.0 <= v <= 1.0)
+        self._max_promote = tunable(max_promote, max_promote_file, int, check=lambda v: v >= 0)
+        self.signal, self.agg = signal, agg
+        self.fp_max = fp_max
         self.stats = collections.Counter()
+
+    @property
+    def tau(self) -> float:
+        from ..utils.tunable import resolve
+        return resolve(self._tau)
+
+    @tau.setter
+    def tau(self, v: float) -> None:         # a fixed value (replaces a file-backed one)
+        self._tau = v
+
+    @property
+    def max_promote(self) -> int:
+        from ..utils.tunable import resolve
+        return resolve(self._max_promote)
+
+    @max_promote.setter
+    def max_promote(self, v: int) -> None:
+        self._max_promote = v
 
     @staticmethod
     def row_stats(logits: torch.Tensor) -> torch.Tensor:
