@@ -76,3 +76,38 @@ def test_env_aliases_of_the_files(monkeypatch):
     monkeypatch.setenv("VLLM_MOE_W2_BASE_MISS_TOL_FILE", "/tmp/tol")
     m = MoetConfig.from_env()
     assert m.gate_tau_file == "/tmp/tau" and m.base_miss_tol_file == "/tmp/tol" and m.gate_max_promote_file is None
+
+
+def _scripted_replay(tmp_path, misses, **kw):
+    import torch
+    from vllm_moet_b200.residency import ExpertCache, ReplayEngine, make_store
+    st = make_store("pinned", 1, 4, 64)
+    st.add_layer(0, torch.zeros(4, 64, dtype=torch.uint8))
+    cache = ExpertCache(st, 1, 4, 64, 2, device="cpu", manager=False)
+    r = ReplayEngine(cache, comm_device="cpu", **kw)
+    seq = iter(misses)
+
+    def step():
+        cache.miss_count += next(seq)
+    return r, r.run(step, lambda: None, lambda: [None])
+
+
+def test_approximate_replay_chases_only_within_fp_thresh(tmp_path):
+    # beyond closing distance after the mandatory first replay: kept (working set moving)
+    r, n = _scripted_replay(tmp_path, [5, 3], mode="approximate", fp_thresh=2, fp_max=8)
+    assert n == 1 and r.stats["fp_giveup"] == 1
+    # within closing distance: chased until miss-free
+    r, n = _scripted_replay(tmp_path, [5, 3, 1, 0], mode="approximate", fp_thresh=4, fp_max=8)
+    assert n == 3 and r.stats["second_order_replays"] == 2 and r.stats["fp_giveup"] == 0
+    # within closing distance but never converging: fp_max, counted, no exception
+    r, n = _scripted_replay(tmp_path, [2] * 10, mode="approximate", fp_thresh=4, fp_max=3)
+    assert n == 3 and r.stats["fp_unfixed"] == 1
+    # the threshold from a file
+    f = str(tmp_path / "th")
+    _write(f, "4", 1)
+    r, n = _scripted_replay(tmp_path, [5, 3, 0], mode="approximate", fp_thresh=0, fp_thresh_file=f, fp_max=8)
+    assert r.fp_thresh == 4 and n == 2
+    # strict mode is untouched: every miss is chased, failing closed at fp_max
+    import pytest
+    with pytest.raises(RuntimeError):
+        _scripted_replay(tmp_path, [2] * 10, mode="strict", fp_max=3)

@@ -226,6 +226,8 @@ class MoetConfig:
     gate_tau_file: Optional[str] = None
     gate_max_promote_file: Optional[str] = None
     base_miss_tol_file: Optional[str] = None
+    fp_thresh: int = 0                  # approximate replay: chase second-order misses while <= this many
+    fp_thresh_file: Optional[str] = None
     # stores
     store_dir: Optional[str] = None
     base_ram_gb: Optional[str] = None
@@ -273,6 +275,8 @@ class MoetConfig:
         "base_cache_gb": "VLLM_MOE_W2_BASE_CACHE_GB",
         "base_miss_tol": "VLLM_MOE_W2_BASE_MISS_TOL",
         "base_miss_tol_file": "VLLM_MOE_W2_BASE_MISS_TOL_FILE",
+        "fp_thresh": "VLLM_MOE_W2_FP_THRESH",
+        "fp_thresh_file": "VLLM_MOE_W2_FP_THRESH_FILE",
         "gate_tau_file": "VLLM_MOE_W2_GATE_TAU_FILE",
         "gate_max_promote_file": "VLLM_MOE_W2_GATE_MAX_PROMOTE_FILE",
         "fp_max": "VLLM_MOE_W2_FP_MAX",

@@ -431,7 +431,8 @@ class LLM:
         self.runner.attach_expert_cache(self.cache)
         self.replay = ReplayEngine(self.cache, tp_group=tp_group, pp_group=self._pp_group, mode=m.replay_mode,
                                    fp_max=m.fp_max,
-                                   miss_tol=m.base_miss_tol, miss_tol_file=m.base_miss_tol_file)
+                                   miss_tol=m.base_miss_tol, miss_tol_file=m.base_miss_tol_file,
+                                   fp_thresh=m.fp_thresh, fp_thresh_file=m.fp_thresh_file)
         self.affinity = DraftAffinity(self.cache) if m.prefetch and self.k > 0 else None
         self.pilot = None
         if m.looka or m.pilot:

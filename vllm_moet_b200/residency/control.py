@@ -50,7 +50,8 @@ class ReplayEngine:
     bitmap stays per stage (reference: PP base segment replay, M5 / M9)."""
 
     def __init__(self, cache: ExpertCache, tp_group=None, mode: str = "strict", fp_max: int = 32,
-                 miss_tol: int = 0, comm_device=None, pp_group=None, miss_tol_file: Optional[str] = None):
+                 miss_tol: int = 0, comm_device=None, pp_group=None, miss_tol_file: Optional[str] = None,
+                 fp_thresh: int = 0, fp_thresh_file: Optional[str] = None):
         if mode not in ("strict", "approximate"):
             raise ValueError(mode)
         from ..utils.tunable import tunable
@@ -60,6 +61,10 @@ class ReplayEngine:
         # runtime-tunable from a file (BASE_MISS_TOL_FILE); the accept decision is reduced
         # across the ranks, so ranks that read a new value one step apart still agree
         self._miss_tol = tunable(miss_tol, miss_tol_file, int, check=lambda v: v >= 0)
+        # approximate mode: after the mandatory first replay, second-order misses are chased
+        # only while at most fp_thresh remain (closing distance); more than that means the
+        # working set is moving and the step is kept (FP_THRESH / FP_THRESH_FILE)
+        self._fp_thresh = tunable(fp_thresh, fp_thresh_file, int, check=lambda v: v >= 0)
         self.comm_device = comm_device or cache.dev
         self.stats = collections.Counter()
 
@@ -71,6 +76,15 @@ class ReplayEngine:
     @miss_tol.setter
     def miss_tol(self, v: int) -> None:      # a fixed value (replaces a file-backed one)
         self._miss_tol = v
+
+    @property
+    def fp_thresh(self) -> int:
+        from ..utils.tunable import resolve
+        return resolve(self._fp_thresh)
+
+    @fp_thresh.setter
+    def fp_thresh(self, v: int) -> None:
+        self._fp_thresh = v
 
     def missing_pairs(self, route_ids: Sequence[Optional[torch.Tensor]]) -> List[Tuple[int, int]]:
         """route_ids[li]: int tensor of routed expert ids of layer li this step (any shape)."""
@@ -122,9 +136,14 @@ class ReplayEngine:
             step()
             misses = self.read_misses()
             self.stats["steps"] += 1
-            if misses == 0 or (self.mode == "approximate" and misses <= self.miss_tol):
+            accept = misses == 0 or (self.mode == "approximate" and misses <= self.miss_tol)
+            if not accept and self.mode == "approximate" and it > 0 and misses > self.fp_thresh:
+                self.stats["fp_giveup"] += 1          # second-order residue beyond closing distance
+                accept = True
+            if accept:
                 self.stats["replays"] += it
                 self.stats["replayed_steps"] += int(it > 0)
+                self.stats["second_order_replays"] += max(it - 1, 0)
                 return it
             pairs = self.missing_pairs(route_ids())
             if not pairs:     # counted misses of experts that are resident by now (a concurrent prefetch)
@@ -134,6 +153,15 @@ class ReplayEngine:
             restore()
         if self.mode == "strict":
             raise RuntimeError(f"expert replay did not converge in {self.fp_max} rounds")
+        # approximate: within closing distance and still not converged -- ping-pong between
+        # evictions; the step keeps the zeroed contributions of the residue (logged, counted)
+        self.stats["fp_unfixed"] += 1
+        self.stats["replays"] += self.fp_max
+        self.stats["replayed_steps"] += 1
+        import logging
+        logging.getLogger("vllm_moet_b200").warning(
+            "expert replay hit fp_max=%d with misses within fp_thresh=%d remaining (ping-pong); step kept",
+            self.fp_max, self.fp_thresh)
         return self.fp_max
 
 
