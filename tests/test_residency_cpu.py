@@ -487,3 +487,45 @@ def _gate_score_tp(rank, world):
 def test_gate_score_tp_ranks_agree():
     res = run_ranks(_gate_score_tp, 3)
     assert all(abs(a - b) < 1e-6 for a, b in res) and len({round(a, 9) for a, _ in res}) == 1
+
+
+def test_warm_state_dump_and_preload_across_boots(tmp_path):
+    """Pool heat and the tiered arena's heat survive a restart: shutdown dumps both, the
+    next boot preheats the arena and preloads the hottest experts into the cold pool; a
+    first boot (no heat files) starts cold."""
+    import types
+    from vllm_moet_b200.config import MoetConfig
+    from vllm_moet_b200.engine.llm import LLM
+    from vllm_moet_b200.residency import ExpertCache, make_store
+    L, E, SB = 2, 8, 512
+
+    def boot():
+        st = make_store("tiered", L, E, SB, dir=str(tmp_path), ckpt_id="ck", arena_rows=8)
+        for li in range(L):
+            if not st.has_layer(li):
+                st.add_layer(li, torch.arange(E * SB, dtype=torch.int32).to(torch.uint8).view(E, SB) + li)
+        cache = ExpertCache(st, L, E, SB, 6, device="cpu", manager=False)
+        ns = types.SimpleNamespace(cache=cache, ecfg=types.SimpleNamespace(moet=MoetConfig()),
+                                   mw=types.SimpleNamespace(tp_rank=0, tp_size=1))
+        ns._heat_path = types.MethodType(LLM._heat_path, ns)
+        return ns
+    a = boot()
+    LLM._warm_start(a, a.ecfg.moet)
+    assert int((a.cache.slot_table >= 0).sum()) == 0                 # first boot: cold
+    a.cache.promote([(0, 3), (1, 5), (1, 6)])
+    a.cache.freq.zero_()
+    a.cache.freq[0, 3], a.cache.freq[1, 5] = 9.0, 4.0
+    LLM._dump_heat(a)
+    assert os.path.exists(LLM._heat_path(a)) and os.path.exists(a.cache.store.heat_path)
+    a.cache.store.release()
+    b = boot()
+    LLM._warm_start(b, b.ecfg.moet)
+    assert b.cache.resident(0, 3) and b.cache.resident(1, 5)
+    assert b.stats_warm["pool_experts"] >= 2 and b.stats_warm["arena_rows"] >= 1
+    b.cache.store.release()
+    # the knobs turn it off
+    c = boot()
+    c.ecfg.moet = MoetConfig(pool_heat=False, tier_preheat=False)
+    LLM._warm_start(c, c.ecfg.moet)
+    assert int((c.cache.slot_table >= 0).sum()) == 0
+    c.cache.store.release()

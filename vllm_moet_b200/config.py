@@ -235,6 +235,9 @@ class MoetConfig:
     store_threads: int = 8
     planes_cache: Optional[str] = None
     ckpt_id: Optional[str] = None
+    pool_heat: bool = True              # dump the expert cache's heat at shutdown, preload it at boot
+    tier_preheat: bool = True           # tiered store: refill the arena from its heat file at boot
+    tier_scan: bool = True              # tiered store: one-shot sweeps bypass the arena
     # tracing and dumps
     prefill_timers_flush: int = 0       # CUDA-event spans of prefill, resolved every N spans (0 = off)
     delta_trace: int = 0                # 1: delta coverage / hit-rate line; 2: + per-layer FP4 histogram
@@ -276,6 +279,9 @@ class MoetConfig:
         "base_miss_tol": "VLLM_MOE_W2_BASE_MISS_TOL",
         "base_miss_tol_file": "VLLM_MOE_W2_BASE_MISS_TOL_FILE",
         "fp_thresh": "VLLM_MOE_W2_FP_THRESH",
+        "pool_heat": "VLLM_MOE_W2_POOL_HEAT",
+        "tier_preheat": "VLLM_MOE_W2_TIER_PREHEAT",
+        "tier_scan": "VLLM_MOE_W2_TIER_SCAN",
         "fp_thresh_file": "VLLM_MOE_W2_FP_THRESH_FILE",
         "gate_tau_file": "VLLM_MOE_W2_GATE_TAU_FILE",
         "gate_max_promote_file": "VLLM_MOE_W2_GATE_MAX_PROMOTE_FILE",

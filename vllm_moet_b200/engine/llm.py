@@ -351,6 +351,7 @@ class LLM:
         release stores and peer buffers."""
         if hasattr(self, "_decode_steps"):
             self.dump_traces()
+        self._dump_heat()
         if getattr(self, "gate_log", None) is not None:
             self.gate_log.close()
             self.gate_log = None
@@ -413,7 +414,7 @@ class LLM:
         if kind in ("pack", "tiered"):
             kw = dict(dir=store_dir or m.store_dir, ckpt_id=m.ckpt_id or checkpoint_id(cfg=self.cfg, seed=self.ecfg.seed),
                       suffix=rank_suffix(self.mw.tp_rank, self.mw.tp_size), direct=m.tier_direct,
-                      threads=m.store_threads)
+                      threads=m.store_threads, scan=m.tier_scan)
             if kw["dir"] is None:
                 raise ValueError("pack / tiered expert stores need a store directory (VLLM_MOE_W2_STORE_DIR)")
         from ..utils.observability import KpiLogger
@@ -429,6 +430,7 @@ class LLM:
                              "(one decode step's routed experts); raise it or set VLLM_MOE_W2_FORCE_POOL=1")
         self.cache = build_expert_cache(self.mw, slots, kind, self.device, **kw)
         self.runner.attach_expert_cache(self.cache)
+        self._warm_start(m)
         self.replay = ReplayEngine(self.cache, tp_group=tp_group, pp_group=self._pp_group, mode=m.replay_mode,
                                    fp_max=m.fp_max,
                                    miss_tol=m.base_miss_tol, miss_tol_file=m.base_miss_tol_file,
@@ -441,6 +443,41 @@ class LLM:
             self.runner.enable_looka(m.pilot_k, m.pilot, self._bucket(self.ecfg.max_num_seqs) * (self.k + 1))
             if m.pilot:
                 self.pilot = Pilot(self.cache, self.runner.pilot_log, m.pilot_cap, m.pilot_min_replay)
+
+    def _heat_path(self):
+        """Where the expert cache's heat lives: beside the pack (pack / tiered stores) or in
+        the store directory; None without either."""
+        st = self.cache.store
+        if getattr(st, "pack_path", None):
+            return st.pack_path[:-5] + ".pool.heat.json"
+        d = self.ecfg.moet.store_dir
+        if d:
+            from ..residency import rank_suffix
+            return os.path.join(d, f"pool.{rank_suffix(self.mw.tp_rank, self.mw.tp_size)}.heat.json")
+        return None
+
+    def _warm_start(self, m):
+        """Warm state at boot (reference: pool heat P:8636-8738, tiered preheat P:13468-13517):
+        the tiered arena refills from its heat file, the expert cache preloads the experts
+        its last run ranked hottest.  Without a heat file the pool starts cold."""
+        st = self.cache.store
+        if m.tier_preheat and hasattr(st, "preheat"):
+            self.stats_warm = {"arena_rows": st.preheat()}
+        path = self._heat_path() if m.pool_heat else None
+        if path and os.path.exists(path):
+            n = self.cache.preload(path)
+            self.stats_warm = dict(getattr(self, "stats_warm", {}), pool_experts=n)
+
+    def _dump_heat(self):
+        m = self.ecfg.moet
+        if getattr(self, "cache", None) is None:
+            return
+        st = self.cache.store
+        if m.tier_preheat and hasattr(st, "dump_heat"):
+            st.dump_heat()
+        path = self._heat_path() if m.pool_heat else None
+        if path:
+            self.cache.dump_heat(path)
 
     # ------------------------------------------------------------------ API
     def _normalize(self, prompts) -> List[List[int]]:

@@ -272,9 +272,10 @@ class MmapPackStore(HostStore):
 class TieredPackStore(MmapPackStore):
     kind = "tiered"
 
-    def __init__(self, *a, arena_rows: int = 64, **kw):
+    def __init__(self, *a, arena_rows: int = 64, scan: bool = True, **kw):
         super().__init__(*a, **kw)
         self.arena_rows = max(1, int(arena_rows))
+        self.scan_enabled = bool(scan)      # False: sweeps go through the arena like any read
         self._arena_raw = _pinned(self.arena_rows * self.stride + ALIGN)
         self._arena_off = (-self._arena_raw.data_ptr()) % ALIGN
         self.lru: "collections.OrderedDict[tuple, int]" = collections.OrderedDict()
@@ -305,7 +306,7 @@ class TieredPackStore(MmapPackStore):
             miss_e = [experts[i] for i in miss_idx]
             protect = {(li, e) for e in experts}
             evictable = len(self.free) + sum(1 for k in self.lru if k not in protect)
-            if scan or len(miss_idx) > evictable:
+            if (scan and self.scan_enabled) or len(miss_idx) > evictable:
                 # scan resistance (and arena overflow): read through the stage, leave the arena as is
                 stage, off = self._stage_rows(len(miss_idx))
                 st = self._read_into(li, miss_e, stage, off, self.stride)
@@ -369,7 +370,7 @@ def make_store(kind: str, n_layers: int, E: int, slot_bytes: int, **kw) -> HostS
     if kind == "tiered":
         return TieredPackStore(kw["dir"], kw.get("tag", "base"), n_layers, E, slot_bytes, kw.get("ckpt_id"),
                                kw.get("suffix"), kw.get("direct", False), kw.get("threads", 8),
-                               arena_rows=kw.get("arena_rows", 64))
+                               arena_rows=kw.get("arena_rows", 64), scan=kw.get("scan", True))
     raise ValueError(f"unknown store kind {kind!r} (pinned | pack | tiered)")
 
 
