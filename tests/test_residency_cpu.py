@@ -529,3 +529,34 @@ def test_warm_state_dump_and_preload_across_boots(tmp_path):
     LLM._warm_start(c, c.ecfg.moet)
     assert int((c.cache.slot_table >= 0).sum()) == 0
     c.cache.store.release()
+
+
+def test_promotion_hysteresis_blocks_near_equal_displacement():
+    """PROMO_HYST: with the delta pool full, a background (tick) candidate displaces a
+    resident only when hotter than h x the weakest evictable resident + 4; mandatory
+    promote() calls are never gated; h = 0 keeps the plain policy."""
+    from vllm_moet_b200.residency.delta import DeltaTier, delta_layout
+    H = I = 64
+    sb = delta_layout(H, I)[0]
+    for h, expect_blocked in ((1.25, True), (0.0, False)):
+        rows = [torch.zeros(4, sb, dtype=torch.uint8) for _ in range(2)]
+        t = DeltaTier(rows, H, I, 2, device="cpu", policy="freq", promo_hyst=h)
+        try:
+            t.promote([(0, 0), (0, 1)])
+            t.step_end()
+            t.freq.zero_()
+            t.freq[0, 0], t.freq[0, 1] = 10.0, 10.0
+            t.freq[1, 2] = 14.0                      # hotter, but < 1.25 x 10 + 4
+            t.tick()
+            t.step_end()
+            assert t.resident(1, 2) != expect_blocked
+            if expect_blocked:
+                assert t.stats["hyst_blocked"] == 1
+                t.freq[1, 2] = 20.0                  # > 16.5: displaces now
+                t.tick()
+                t.step_end()
+                assert t.resident(1, 2)
+                t.promote([(1, 3)])                  # mandatory: never gated
+                assert t.resident(1, 3)
+        finally:
+            t.close()

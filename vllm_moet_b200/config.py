@@ -207,6 +207,7 @@ class MoetConfig:
     delta_tick_ms: float = 50.0
     prefill_fp4: str = "1"              # "1": prefill serves delta-slot experts at FP4 too; "0": base only
     delta_decay: float = 0.98
+    promo_hyst: float = 0.0             # > 1: background promotions into a full pool need freq > h x victim + 4
     # base cache (GPU as expert cache)
     base_cache_gb: float = 0.0
     base_miss_tol: int = 0
@@ -275,6 +276,7 @@ class MoetConfig:
         "delta_tick_ms": "VLLM_MOE_W2_DELTA_TICK_MS",
         "prefill_fp4": "VLLM_MOE_W2_PREFILL_FP4",
         "delta_decay": "VLLM_MOE_W2_DELTA_DECAY",
+        "promo_hyst": "VLLM_MOE_W2_PROMO_HYST",
         "base_cache_gb": "VLLM_MOE_W2_BASE_CACHE_GB",
         "base_miss_tol": "VLLM_MOE_W2_BASE_MISS_TOL",
         "base_miss_tol_file": "VLLM_MOE_W2_BASE_MISS_TOL_FILE",

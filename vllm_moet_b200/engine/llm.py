@@ -374,7 +374,7 @@ class LLM:
             raise ValueError("delta tier needs weights built with delta rows")
         lay = layers[0].experts.layout
         self.delta = DeltaTier(rows, lay.H, lay.I, slots, device=self.device, policy=m.delta_policy,
-                               decay=m.delta_decay, split=m.delta_split)
+                               decay=m.delta_decay, split=m.delta_split, promo_hyst=m.promo_hyst)
         if getattr(self, "cache", None) is not None:
             self.delta.couple(self.cache)
         for lw in layers:

@@ -89,7 +89,7 @@ def dequant_delta_slot(row: torch.Tensor, H: int, I: int):
 
 class DeltaTier(ExpertCache):
     def __init__(self, rows_per_layer: List[torch.Tensor], H: int, I: int, n_slots: int, device="cuda",
-                 policy: str = "freq", decay: float = 0.98, split: bool = False):
+                 policy: str = "freq", decay: float = 0.98, split: bool = False, promo_hyst: float = 0.0):
         L = len(rows_per_layer)
         E = rows_per_layer[0].shape[0]
         self.split = split
@@ -102,6 +102,11 @@ class DeltaTier(ExpertCache):
         super().__init__(store, L, E, sb, n_slots, device=device, policy="lru" if policy == "lru" else "freq",
                          decay=decay, manager=True)
         self.delta_policy = policy
+        # promotion hysteresis (PROMO_HYST = h > 1): with the pool full, a background candidate
+        # displaces a resident expert only when its decayed frequency exceeds h x the weakest
+        # evictable resident's + 4, so a drifting working set does not ping-pong slots.
+        # Mandatory promotions (gate fires, misses) call promote() directly and are never gated.
+        self.promo_hyst = float(promo_hyst)
 
     def couple(self, base_cache) -> None:
         """Split FP4 over a base expert cache: promotions make the base resident
@@ -136,4 +141,26 @@ class DeltaTier(ExpertCache):
                     want.append((li, e))
                 if len(want) >= max_promote:
                     break
+            want = self._hysteresis(want)
         return self.promote(want) if want else 0
+
+    def _hysteresis(self, want):
+        """Drop the candidates that would only displace a near-equal resident (see promo_hyst)."""
+        h = self.promo_hyst
+        if h <= 1.0 or not want:
+            return want
+        n_free = len(self.free)
+        victims = sorted(float(self.freq[o[0], o[1]]) for s, o in enumerate(self.owner)
+                         if o is not None and s not in self.pinned
+                         and not (self.protect is not None and self.protect(*o)))
+        kept, vi = [], 0
+        for li, e in want:                          # hottest first
+            if n_free > 0:
+                n_free -= 1
+                kept.append((li, e))
+            elif vi < len(victims) and float(self.freq[li, e]) > h * victims[vi] + 4.0:
+                vi += 1
+                kept.append((li, e))
+            else:
+                self.stats["hyst_blocked"] += 1
+        return kept
