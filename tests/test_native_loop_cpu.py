@@ -428,3 +428,44 @@ def test_allowed_token_ids_in_the_gpu_loop(engine):
     out = llm.generate([[5, 6, 7], [9, 10]], [SamplingParams(max_tokens=6, ignore_eos=True), only])
     assert out[0].outputs[0].token_ids == chain([5, 6, 7], 6)
     assert set(out[1].outputs[0].token_ids) <= {77, 78} and len(out[1].outputs[0].token_ids) == 6
+
+
+def test_gate_audit_spec_mask_and_trace(engine, tmp_path, caplog):
+    """GATE_AUDIT = 1 with a gate that never fires: every step with experts to promote runs
+    one audit fire (promote + replay) logged with its argmax flips; GATE_SPEC_MASK scores only the emitted verify
+    rows; GATE_TRACE logs each fire.  Output is still the model's chain."""
+    import json
+    import logging
+    from vllm_moet_b200.residency import ConfidenceGate
+    from vllm_moet_b200.residency.delta import DeltaTier, delta_layout
+    from vllm_moet_b200.utils.observability import JsonlWriter
+    llm = engine()
+    L, E, H, I = 2, 8, 64, 64
+    sb = delta_layout(H, I)[0]
+    llm.delta = DeltaTier([torch.zeros(E, sb, dtype=torch.uint8) for _ in range(L)], H, I, 16, device="cpu",
+                          policy="need")
+    llm.gate = ConfidenceGate(tau=-1.0, fp_max=2)          # never fires on its own
+    llm.delta_trace = None
+    llm.gate_log = JsonlWriter(str(tmp_path / "gate.jsonl"))
+    m = llm.ecfg.moet
+    m.gate_fire_timing, m.gate_audit, m.gate_spec_mask, m.gate_trace = False, 1.0, True, True
+    llm.runner.route_ids = lambda B, st=None: [torch.tensor([[int(t) % E, (int(t) + 1) % E] for t in
+                                                             llm._states[B].tokens[:, 0].tolist()])] * L
+    scored = []
+    real_score = llm.gate.score
+    llm.gate.score = lambda lg, tp_group=None: (scored.append(lg.shape[0]), real_score(lg, tp_group=tp_group))[1]
+    try:
+        with caplog.at_level(logging.INFO, logger="vllm_moet_b200"):
+            out = llm.generate([[5, 6, 7]], SamplingParams(max_tokens=10, ignore_eos=True))[0].outputs[0].token_ids
+    finally:
+        llm.delta.close()
+        llm.gate_log.close()
+    assert out == chain([5, 6, 7], 10)
+    rows = [json.loads(x) for x in (tmp_path / "gate.jsonl").read_text().splitlines()]
+    # every fire is an audit (one per step; none once the step's experts are all resident)
+    fired = [r for r in rows if r["fired"]]
+    assert fired and all(r["audit"] and r["fired"] == 1 and "flips" in r for r in fired)
+    assert all(not r["audit"] for r in rows if not r["fired"])
+    assert llm.delta.stats["gate_audits"] == len(fired)
+    assert max(scored) <= llm.k + 1 and min(scored) >= 1            # emitted rows of one sequence
+    assert any("gate audit" in r.getMessage() for r in caplog.records)

@@ -223,6 +223,9 @@ class MoetConfig:
     gate_agg: str = "min"               # min | q<frac>
     gate_fp_max: int = 3
     gate_max_promote: int = 64
+    gate_spec_mask: bool = False        # score only the verify rows the step emits (skip rows past a rejection)
+    gate_trace: bool = False            # log every fire / re-forward
+    gate_audit: float = 0.0             # probability of an audit fire on a confident step (unbiased labels)
     # runtime-tunable knobs: a one-line file re-read when it changes (path or None)
     gate_tau_file: Optional[str] = None
     gate_max_promote_file: Optional[str] = None
@@ -277,6 +280,9 @@ class MoetConfig:
         "prefill_fp4": "VLLM_MOE_W2_PREFILL_FP4",
         "delta_decay": "VLLM_MOE_W2_DELTA_DECAY",
         "promo_hyst": "VLLM_MOE_W2_PROMO_HYST",
+        "gate_spec_mask": "VLLM_MOE_W2_GATE_SPEC_MASK",
+        "gate_trace": "VLLM_MOE_W2_GATE_TRACE",
+        "gate_audit": "VLLM_MOE_W2_GATE_AUDIT",
         "base_cache_gb": "VLLM_MOE_W2_BASE_CACHE_GB",
         "base_miss_tol": "VLLM_MOE_W2_BASE_MISS_TOL",
         "base_miss_tol_file": "VLLM_MOE_W2_BASE_MISS_TOL_FILE",

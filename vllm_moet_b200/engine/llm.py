@@ -1162,10 +1162,19 @@ class LLM:
         if self.delta_trace is not None:
             self.delta_trace.step(self.delta, self._routed_token_counts(B))
         if self.gate is not None:
-            rows = torch.nonzero(st.active_rows).flatten()
+            m = self.ecfg.moet
             logits = self.runner.main_logits(B)
             step = (graph.replay if graph is not None else (lambda: self._decode_eager(st)))
             snap = self._delta_snap
+
+            def gate_rows():
+                # the verify rows the gate scores: every active row, or with GATE_SPEC_MASK only
+                # the rows the step emits (a row past the first rejected draft is discarded)
+                act = st.active_rows.reshape(-1).bool()
+                if m.gate_spec_mask and self.k > 0:
+                    act = act & (st.arange_kp1[None, :] <= st.n_acc.reshape(-1, 1)).reshape(-1)
+                return torch.nonzero(act).flatten()
+            rows = gate_rows()
 
             def run_step():
                 st.restore(snap)
@@ -1174,7 +1183,7 @@ class LLM:
                     self.replay.run(step, lambda: st.restore(snap), lambda: self.runner.route_ids(B))
                 else:
                     step()
-                return logits[rows] if logits is not None else None     # no head before the last PP stage
+                return logits[gate_rows()] if logits is not None else None   # no head before the last PP stage
             if self._pp_group is not None:
                 fired = self._pp_gate(B, run_step, lambda: self.gate.score(logits[rows], tp_group=self._tp_group))
                 self.delta.stats["gate_replays"] += fired
@@ -1184,7 +1193,12 @@ class LLM:
             score = self.gate.score(logits[rows], tp_group=self._tp_group)
             score0, fired, iters = score, 0, []
             timing = self.ecfg.moet.gate_fire_timing
-            while fired < self.gate.fp_max and self.gate.should_fire(score):
+            pre = logits[rows].argmax(-1).cpu() if logits is not None else None
+            # audit: a confident step fires anyway with probability p, so the logged flips give
+            # unbiased labels of what the gate misses; a seeded generator, the same on every rank
+            audit = (m.gate_audit > 0 and not self.gate.should_fire(score)
+                     and self._audit_rng().random() < m.gate_audit)
+            while fired < self.gate.fp_max and (self.gate.should_fire(score) or (audit and fired == 0)):
                 promote = [p for p in self._routed_pairs(B) if not self.delta.resident(*p)][: self.gate.max_promote]
                 t0 = time.perf_counter()
                 # fail-safe: a failed host read on any TP rank means no rank replays
@@ -1203,13 +1217,30 @@ class LLM:
                     it.update(promote_ms=(t1 - t0) * 1e3, replay_ms=e0.elapsed_time(e1))
                 iters.append(it)
                 fired += 1
+                if m.gate_trace:
+                    import logging
+                    logging.getLogger("vllm_moet_b200").info(
+                        "gate %s step %d: score %.4f -> %.4f (tau %.3f), promoted %d",
+                        "audit" if audit else "fire", self._decode_steps, score0, score, self.gate.tau, len(promote))
             self.delta.stats["gate_replays"] += fired
+            self.delta.stats["gate_audits"] += int(audit and fired > 0)
             if self.gate_log is not None:
-                self.gate_log.write({"step": self._decode_steps, "score": score0, "tau": self.gate.tau,
-                                     "fired": fired, "final_score": score, "iters": iters})
+                rec = {"step": self._decode_steps, "score": score0, "tau": self.gate.tau,
+                       "fired": fired, "final_score": score, "iters": iters, "audit": bool(audit and fired > 0)}
+                if fired and pre is not None:
+                    post = logits[gate_rows()].argmax(-1).cpu()
+                    n = min(len(pre), len(post))
+                    rec["flips"] = int((pre[:n] != post[:n]).sum())
+                self.gate_log.write(rec)
         else:
             self.delta.tick()
         self.delta.step_end()
+
+    def _audit_rng(self):
+        import random
+        if getattr(self, "_gate_audit_rng", None) is None:
+            self._gate_audit_rng = random.Random(self.ecfg.seed * 7919 + 17)
+        return self._gate_audit_rng
 
     def _pp_gate(self, B, run_step, score_fn) -> int:
         """The gate under pipeline parallelism: only the last stage has the verify logits,
