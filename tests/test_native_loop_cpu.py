@@ -469,3 +469,41 @@ def test_gate_audit_spec_mask_and_trace(engine, tmp_path, caplog):
     assert llm.delta.stats["gate_audits"] == len(fired)
     assert max(scored) <= llm.k + 1 and min(scored) >= 1            # emitted rows of one sequence
     assert any("gate audit" in r.getMessage() for r in caplog.records)
+
+
+@pytest.mark.parametrize("mode", ["capture", "no_reforward"])
+def test_gate_capture_and_no_reforward(engine, tmp_path, mode):
+    """GATE_CAPTURE: an always-firing gate only logs (no promotion, no replay).
+    GATE_REFORWARD=0: a fire promotes for later steps but the step is not replayed."""
+    import json
+    from vllm_moet_b200.residency import ConfidenceGate
+    from vllm_moet_b200.residency.delta import DeltaTier, delta_layout
+    from vllm_moet_b200.utils.observability import JsonlWriter
+    llm = engine()
+    L, E, H, I = 2, 8, 64, 64
+    sb = delta_layout(H, I)[0]
+    llm.delta = DeltaTier([torch.zeros(E, sb, dtype=torch.uint8) for _ in range(L)], H, I, 16, device="cpu",
+                          policy="need")
+    llm.gate = ConfidenceGate(tau=2.0, fp_max=2)
+    llm.delta_trace = None
+    llm.gate_log = JsonlWriter(str(tmp_path / "gate.jsonl"))
+    m = llm.ecfg.moet
+    m.gate_fire_timing = False
+    m.gate_capture, m.gate_reforward = mode == "capture", mode != "no_reforward"
+    llm.runner.route_ids = lambda B, st=None: [torch.tensor([[int(t) % E, (int(t) + 1) % E] for t in
+                                                             llm._states[B].tokens[:, 0].tolist()])] * L
+    try:
+        out = llm.generate([[5, 6, 7]], SamplingParams(max_tokens=8, ignore_eos=True))[0].outputs[0].token_ids
+    finally:
+        llm.delta.close()
+        llm.gate_log.close()
+    assert out == chain([5, 6, 7], 8)
+    rows = [json.loads(x) for x in (tmp_path / "gate.jsonl").read_text().splitlines()]
+    assert llm.delta.stats["gate_replays"] == 0                     # neither mode replays a step
+    if mode == "capture":
+        assert rows and all(r["capture"] and r["would_fire"] for r in rows)
+        assert llm.delta.stats["fetched_rows"] == 0
+    else:
+        fired = [r for r in rows if r["fired"]]
+        assert fired and all(r["iters"][0]["reforward"] is False for r in fired)
+        assert llm.delta.stats["fetched_rows"] > 0 and llm.delta.stats["gate_promote_only"] == len(fired)

@@ -560,3 +560,14 @@ def test_promotion_hysteresis_blocks_near_equal_displacement():
                 assert t.resident(1, 3)
         finally:
             t.close()
+
+
+def test_delta_pool_sizing_from_gib_or_auto():
+    from vllm_moet_b200.residency.delta import delta_slots_for
+    G = 1 << 30
+    assert delta_slots_for("2", 1 << 20, 0) == 2048
+    assert delta_slots_for("auto", 1 << 20, 10 * G, reserve_gb=3.0) == 7 * 1024
+    assert delta_slots_for("auto", 1 << 20, 10 * G, reserve_gb=3.0, max_gb=1.5) == 1536
+    assert delta_slots_for("auto", 1 << 20, 2 * G, reserve_gb=3.0) == 0
+    with pytest.raises(ValueError):
+        delta_slots_for("lots", 1 << 20, G)

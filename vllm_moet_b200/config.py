@@ -202,6 +202,9 @@ class MoetConfig:
     # FP4 delta tier
     delta: bool = False
     delta_gb: str = "0"                 # "N" GiB or "auto"
+    delta_reserve_gb: float = 3.0       # auto: HBM left free beside the delta pool
+    delta_max_gb: float = 0.0           # auto: cap of the pool (0 = none)
+    delta_promote: int = 64             # background promotions per tick (the reference defaults to 8)
     delta_policy: str = "freq"          # freq | need | lru
     delta_split: bool = False
     delta_tick_ms: float = 50.0
@@ -226,6 +229,8 @@ class MoetConfig:
     gate_spec_mask: bool = False        # score only the verify rows the step emits (skip rows past a rejection)
     gate_trace: bool = False            # log every fire / re-forward
     gate_audit: float = 0.0             # probability of an audit fire on a confident step (unbiased labels)
+    gate_reforward: bool = True         # False: a fire promotes for later steps but does not replay this one
+    gate_capture: bool = False          # measurement only: score and log, never promote or replay
     # runtime-tunable knobs: a one-line file re-read when it changes (path or None)
     gate_tau_file: Optional[str] = None
     gate_max_promote_file: Optional[str] = None
@@ -274,6 +279,9 @@ class MoetConfig:
         "zero_mode": "VLLM_MOE_W2_ZERO_MODE",
         "delta": "VLLM_MOE_W2_DELTA",
         "delta_gb": "VLLM_MOE_W2_DELTA_GB",
+        "delta_reserve_gb": "VLLM_MOE_W2_DELTA_RESERVE_GB",
+        "delta_max_gb": "VLLM_MOE_W2_DELTA_MAX_GB",
+        "delta_promote": "VLLM_MOE_W2_DELTA_PROMOTE",
         "delta_policy": "VLLM_MOE_W2_DELTA_POLICY",
         "delta_split": "VLLM_MOE_W2_DELTA_SPLIT",
         "delta_tick_ms": "VLLM_MOE_W2_DELTA_TICK_MS",
@@ -283,6 +291,8 @@ class MoetConfig:
         "gate_spec_mask": "VLLM_MOE_W2_GATE_SPEC_MASK",
         "gate_trace": "VLLM_MOE_W2_GATE_TRACE",
         "gate_audit": "VLLM_MOE_W2_GATE_AUDIT",
+        "gate_reforward": "VLLM_MOE_W2_GATE_REFORWARD",
+        "gate_capture": "VLLM_MOE_W2_GATE_CAPTURE",
         "base_cache_gb": "VLLM_MOE_W2_BASE_CACHE_GB",
         "base_miss_tol": "VLLM_MOE_W2_BASE_MISS_TOL",
         "base_miss_tol_file": "VLLM_MOE_W2_BASE_MISS_TOL_FILE",

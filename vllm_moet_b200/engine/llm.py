@@ -235,6 +235,15 @@ class LLM:
             if slots:
                 self._attach_cache(slots, expert_store, expert_store_dir, tp_group)
             self.delta = self.gate = None
+            m = self.ecfg.moet
+            if not delta_slots and m.delta and str(m.delta_gb) not in ("0", ""):
+                # VLLM_MOE_W2_DELTA=1 with a size in GiB or auto (free HBM after load - reserve)
+                from ..residency import moe_layers
+                from ..residency.delta import delta_layout, delta_slots_for
+                lay = moe_layers(self.mw)[0].experts.layout
+                free = torch.cuda.mem_get_info(self.device)[0]
+                delta_slots = delta_slots_for(m.delta_gb, delta_layout(lay.H, lay.I)[0], free,
+                                              m.delta_reserve_gb, m.delta_max_gb)
             if delta_slots:
                 self._attach_delta(delta_slots, gate)
             trellis_pack = trellis_pack or os.environ.get("VLLM_MOE_W2_EXL3_PACK") or None
@@ -1198,6 +1207,12 @@ class LLM:
             # unbiased labels of what the gate misses; a seeded generator, the same on every rank
             audit = (m.gate_audit > 0 and not self.gate.should_fire(score)
                      and self._audit_rng().random() < m.gate_audit)
+            if m.gate_capture:     # measurement mode: the decision is logged, nothing changes
+                if self.gate_log is not None:
+                    self.gate_log.write({"step": self._decode_steps, "score": score0, "tau": self.gate.tau,
+                                         "would_fire": bool(self.gate.should_fire(score)), "capture": True})
+                self.delta.step_end()
+                return
             while fired < self.gate.fp_max and (self.gate.should_fire(score) or (audit and fired == 0)):
                 promote = [p for p in self._routed_pairs(B) if not self.delta.resident(*p)][: self.gate.max_promote]
                 t0 = time.perf_counter()
@@ -1209,6 +1224,10 @@ class LLM:
                 if timing:
                     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     e0.record()
+                if not m.gate_reforward:     # promoted for the next steps; this step stands
+                    iters.append({"promoted": len(promote), "reforward": False})
+                    fired += 1
+                    break
                 score = self.gate.score(run_step(), tp_group=self._tp_group)
                 it = {"promoted": len(promote), "score": score}
                 if timing:
@@ -1222,7 +1241,10 @@ class LLM:
                     logging.getLogger("vllm_moet_b200").info(
                         "gate %s step %d: score %.4f -> %.4f (tau %.3f), promoted %d",
                         "audit" if audit else "fire", self._decode_steps, score0, score, self.gate.tau, len(promote))
-            self.delta.stats["gate_replays"] += fired
+            if m.gate_reforward:
+                self.delta.stats["gate_replays"] += fired
+            else:
+                self.delta.stats["gate_promote_only"] += fired
             self.delta.stats["gate_audits"] += int(audit and fired > 0)
             if self.gate_log is not None:
                 rec = {"step": self._decode_steps, "score": score0, "tau": self.gate.tau,
@@ -1233,7 +1255,7 @@ class LLM:
                     rec["flips"] = int((pre[:n] != post[:n]).sum())
                 self.gate_log.write(rec)
         else:
-            self.delta.tick()
+            self.delta.tick(self.ecfg.moet.delta_promote)
         self.delta.step_end()
 
     def _audit_rng(self):

@@ -35,6 +35,27 @@ from .stores import make_store
 from .tier import ExpertCache
 
 
+def delta_slots_for(delta_gb: str, slot_bytes: int, free_bytes: int, reserve_gb: float = 3.0,
+                    max_gb: float = 0.0) -> int:
+    """Delta-pool size in slots from ``VLLM_MOE_W2_DELTA_GB``: ``"N"`` GiB, or ``"auto"``
+    (the free device memory after load minus ``reserve_gb``, capped by ``max_gb`` when
+    non-zero).  Reference: delta sizing, patch P:7903-7916."""
+    g = 1 << 30
+    v = str(delta_gb).strip().lower()
+    if v == "auto":
+        budget = max(0, int(free_bytes) - int(reserve_gb * g))
+        if max_gb > 0:
+            budget = min(budget, int(max_gb * g))
+    else:
+        try:
+            budget = int(float(v) * g)
+        except ValueError:
+            raise ValueError(f"VLLM_MOE_W2_DELTA_GB must be a number of GiB or auto, got {delta_gb!r}") from None
+        if budget < 0:
+            raise ValueError("VLLM_MOE_W2_DELTA_GB must be >= 0")
+    return budget // int(slot_bytes)
+
+
 def delta_layout(H: int, I: int):
     """-> (slot_bytes, codes13, sc13, codes2, sc2 offsets) of a direct-8 delta slot."""
     c13 = planes.direct8_plane_bytes(2 * I, H)
