@@ -507,3 +507,30 @@ def test_gate_capture_and_no_reforward(engine, tmp_path, mode):
         fired = [r for r in rows if r["fired"]]
         assert fired and all(r["iters"][0]["reforward"] is False for r in fired)
         assert llm.delta.stats["fetched_rows"] > 0 and llm.delta.stats["gate_promote_only"] == len(fired)
+
+
+def test_capped_gate_fire_promotes_the_most_needed_first(engine):
+    """With more routed experts than gate max_promote, a fire promotes the ones the delta
+    tier ranks highest (its decayed need / frequency)."""
+    from vllm_moet_b200.residency import ConfidenceGate
+    from vllm_moet_b200.residency.delta import DeltaTier, delta_layout
+    llm = engine()
+    L, E, H, I = 2, 8, 64, 64
+    sb = delta_layout(H, I)[0]
+    llm.delta = DeltaTier([torch.zeros(E, sb, dtype=torch.uint8) for _ in range(L)], H, I, 16, device="cpu",
+                          policy="need")
+    llm.gate = ConfidenceGate(tau=2.0, fp_max=1, max_promote=1)
+    llm.delta_trace, llm.gate_log = None, None
+    llm.ecfg.moet.gate_fire_timing = False
+    llm.runner.route_ids = lambda B, st=None: [torch.tensor([[int(t) % E, (int(t) + 1) % E] for t in
+                                                             llm._states[B].tokens[:, 0].tolist()])] * L
+    llm.delta.freq[1, :] = torch.arange(E, dtype=torch.float32) * 100.0    # layer 1, higher ids hotter
+    calls = []
+    real = llm.delta.promote
+    llm.delta.promote = lambda pairs, **kw: (calls.append(list(pairs)), real(pairs, **kw))[1]
+    try:
+        llm.generate([[5, 6, 7]], SamplingParams(max_tokens=2, ignore_eos=True))
+    finally:
+        llm.delta.close()
+    first = calls[0]
+    assert len(first) == 1 and first[0][0] == 1            # a layer-1 expert, the hottest routed one

@@ -1214,7 +1214,13 @@ class LLM:
                 self.delta.step_end()
                 return
             while fired < self.gate.fp_max and (self.gate.should_fire(score) or (audit and fired == 0)):
-                promote = [p for p in self._routed_pairs(B) if not self.delta.resident(*p)][: self.gate.max_promote]
+                promote = [p for p in self._routed_pairs(B) if not self.delta.resident(*p)]
+                if len(promote) > self.gate.max_promote:
+                    # a binding cap promotes the most-needed experts first (the tier's decayed
+                    # rank: repeat offenders across fires), ties in routing order
+                    fq = self.delta.freq
+                    promote = sorted(promote, key=lambda p: -float(fq[p[0], p[1]]))
+                promote = promote[: self.gate.max_promote]
                 t0 = time.perf_counter()
                 # fail-safe: a failed host read on any TP rank means no rank replays
                 if not gate_promote_consensus(lambda: self.delta.promote(promote) if promote else 0,
