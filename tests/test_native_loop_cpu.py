@@ -534,3 +534,38 @@ def test_capped_gate_fire_promotes_the_most_needed_first(engine):
         llm.delta.close()
     first = calls[0]
     assert len(first) == 1 and first[0][0] == 1            # a layer-1 expert, the hottest routed one
+
+
+def test_gate_hidden_capture_shards(engine, tmp_path):
+    """GATE_HCAP_DIR with the gate dump: the scored rows' hidden states of every fired step
+    go to hcap-NNNNN.pt shards (flushed every GATE_HCAP_FLUSH records and at close), keyed
+    by the dump's step numbers."""
+    import json
+    from vllm_moet_b200.residency import ConfidenceGate
+    from vllm_moet_b200.residency.delta import DeltaTier, delta_layout
+    from vllm_moet_b200.utils.observability import HiddenCapture, JsonlWriter
+    llm = engine()
+    L, E, H, I = 2, 8, 64, 64
+    sb = delta_layout(H, I)[0]
+    llm.delta = DeltaTier([torch.zeros(E, sb, dtype=torch.uint8) for _ in range(L)], H, I, 16, device="cpu",
+                          policy="need")
+    llm.gate = ConfidenceGate(tau=2.0, fp_max=1)
+    llm.delta_trace = None
+    llm.gate_log = JsonlWriter(str(tmp_path / "gate.jsonl"))
+    llm.hcap = HiddenCapture(str(tmp_path / "hcap"), flush=2)
+    llm.ecfg.moet.gate_fire_timing = False
+    llm.runner.main_hidden = lambda B: torch.arange(B * (llm.k + 1) * 4, dtype=torch.float32).view(-1, 4)
+    llm.runner.route_ids = lambda B, st=None: [torch.tensor([[int(t) % E, (int(t) + 1) % E] for t in
+                                                             llm._states[B].tokens[:, 0].tolist()])] * L
+    try:
+        llm.generate([[5, 6, 7]], SamplingParams(max_tokens=8, ignore_eos=True))
+    finally:
+        llm.delta.close()
+        llm.gate_log.close()
+        llm.hcap.close()
+    fired = [r["step"] for r in map(json.loads, (tmp_path / "gate.jsonl").read_text().splitlines()) if r["fired"]]
+    shards = sorted((tmp_path / "hcap").glob("hcap-*.pt"))
+    got = [torch.load(p) for p in shards]
+    steps = sum((g["steps"].tolist() for g in got), [])
+    assert fired and steps == fired and len(shards) == (len(fired) + 1) // 2
+    assert all(h.shape[1] == 4 for g in got for h in g["h"])

@@ -231,6 +231,8 @@ class MoetConfig:
     gate_audit: float = 0.0             # probability of an audit fire on a confident step (unbiased labels)
     gate_reforward: bool = True         # False: a fire promotes for later steps but does not replay this one
     gate_capture: bool = False          # measurement only: score and log, never promote or replay
+    gate_hcap_dir: Optional[str] = None  # with the gate dump: hidden states of fired / audited steps
+    gate_hcap_flush: int = 256
     # runtime-tunable knobs: a one-line file re-read when it changes (path or None)
     gate_tau_file: Optional[str] = None
     gate_max_promote_file: Optional[str] = None
@@ -293,6 +295,8 @@ class MoetConfig:
         "gate_audit": "VLLM_MOE_W2_GATE_AUDIT",
         "gate_reforward": "VLLM_MOE_W2_GATE_REFORWARD",
         "gate_capture": "VLLM_MOE_W2_GATE_CAPTURE",
+        "gate_hcap_dir": "VLLM_MOE_W2_GATE_HCAP_DIR",
+        "gate_hcap_flush": "VLLM_MOE_W2_GATE_HCAP_FLUSH",
         "base_cache_gb": "VLLM_MOE_W2_BASE_CACHE_GB",
         "base_miss_tol": "VLLM_MOE_W2_BASE_MISS_TOL",
         "base_miss_tol_file": "VLLM_MOE_W2_BASE_MISS_TOL_FILE",

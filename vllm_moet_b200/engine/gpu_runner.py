@@ -552,6 +552,15 @@ class NativeRunner:
         if not self._moe_index:
             self._moe_index = {id(lw): i for i, lw in enumerate(moe_layers(self.mw))}
 
+    def main_hidden(self, B: int):
+        """Final normed hidden states [B*(1+k), H] of bucket B's last decode step (None where
+        this rank has no head)."""
+        b = self._bucket_ws(B).bufs.get(("main.hid", torch.bfloat16))
+        if b is None:
+            return None
+        H = self.cfg.hidden
+        return b[: B * (self.k + 1) * H].view(B * (self.k + 1), H)
+
     def main_logits(self, B: int):
         """Logits [B*(1+k), V] of the last decode step of bucket B (verify rows, row i*(k+1)+j);
         None where this rank has no head (PP stages before the last).  V is this rank's

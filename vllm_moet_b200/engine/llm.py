@@ -313,6 +313,8 @@ class LLM:
         self.delta_trace = (obs.DeltaTrace(level=m.delta_trace, every=m.kpi_every)
                             if m.delta_trace and self.delta is not None else None)
         self.gate_log = obs.JsonlWriter(m.gate_dump) if m.gate_dump and self.gate is not None else None
+        self.hcap = (obs.HiddenCapture(m.gate_hcap_dir, m.gate_hcap_flush)
+                     if self.gate_log is not None and m.gate_hcap_dir else None)
         self._decode_steps = 0
 
     def dump_traces(self):
@@ -364,6 +366,9 @@ class LLM:
         if getattr(self, "gate_log", None) is not None:
             self.gate_log.close()
             self.gate_log = None
+        if getattr(self, "hcap", None) is not None:
+            self.hcap.close()
+            self.hcap = None
         for tier in (getattr(self, "delta", None), getattr(self, "cache", None)):
             if tier is not None:
                 tier.close()
@@ -1260,6 +1265,11 @@ class LLM:
                     n = min(len(pre), len(post))
                     rec["flips"] = int((pre[:n] != post[:n]).sum())
                 self.gate_log.write(rec)
+                hid = getattr(self.runner, "main_hidden", None)
+                if fired and getattr(self, "hcap", None) is not None and hid is not None:
+                    h = hid(B)
+                    if h is not None:
+                        self.hcap.store(self._decode_steps, h[gate_rows()])
         else:
             self.delta.tick(self.ecfg.moet.delta_promote)
         self.delta.step_end()

@@ -187,6 +187,39 @@ class JsonlWriter:
         self.f.close()
 
 
+class HiddenCapture:
+    """Hidden states of the gate's dumped (fired / audited) steps, for offline gate-signal
+    studies: ``store(step, h)`` keeps one [rows, H] tensor per step, every ``flush``
+    records a shard ``hcap-NNNNN.pt`` = {"steps": int64 [n], "h": list of tensors} goes to
+    ``dir``; consumers join on the gate dump's ``step`` field.  (Reference: the gate's
+    hidden-state capture, VLLM_MOE_W2_GATE_HCAP_DIR / _FLUSH, patch P:11384-11420.)"""
+
+    def __init__(self, dir_: str, flush: int = 256):
+        self.dir, self.flush_every = dir_, max(1, int(flush))
+        self.steps: List[int] = []
+        self.h: List[torch.Tensor] = []
+        self.shard = 0
+
+    def store(self, step: int, h: torch.Tensor):
+        self.steps.append(int(step))
+        self.h.append(h.detach().to("cpu", torch.float32))
+        if len(self.steps) >= self.flush_every:
+            self.flush()
+
+    def flush(self):
+        if not self.steps:
+            return
+        os.makedirs(self.dir, exist_ok=True)
+        path = os.path.join(self.dir, f"hcap-{self.shard:05d}.pt")
+        torch.save({"steps": torch.tensor(self.steps, dtype=torch.int64), "h": self.h}, path + ".tmp")
+        os.replace(path + ".tmp", path)
+        self.shard += 1
+        self.steps, self.h = [], []
+
+    def close(self):
+        self.flush()
+
+
 class SpanTimers:
     def __init__(self, flush_every: int = 64, sink=None):
         self.flush_every = flush_every
