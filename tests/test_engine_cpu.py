@@ -361,3 +361,11 @@ def test_allowed_token_ids_match_masked_greedy(tiny_llm):
 def test_get_tokenizer(tiny_llm):
     tok = tiny_llm.get_tokenizer()
     assert tok is tiny_llm.tokenizer and tok.decode(tok.encode("ab")) == "ab"
+
+
+def test_request_acceptance_metrics(tiny_llm):
+    """Per-request acceptance length: tokens emitted per decode step after the first token."""
+    o = tiny_llm.generate([[5, 9, 17, 33]], SamplingParams(max_tokens=10, ignore_eos=True))[0]
+    m = o.metrics
+    assert m["decode_steps"] >= 1 and 1.0 <= m["tokens_per_step"] <= tiny_llm.k + 1
+    assert abs(m["tokens_per_step"] * m["decode_steps"] - (len(o.outputs[0].token_ids) - 1)) < 1e-9

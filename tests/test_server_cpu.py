@@ -92,6 +92,8 @@ def test_completions_match_engine(server):
     count = [ln for ln in m.splitlines() if ln.startswith("moet_e2e_request_latency_seconds_count")][0]
     assert float(count.split()[-1]) >= 1
     assert "moet_decode_steps_total" in m and "moet_accepted_draft_tokens_total" in m
+    acc = [ln for ln in m.splitlines() if ln.startswith("moet_request_tokens_per_step_count")][0]
+    assert float(acc.split()[-1]) >= 1
 
 
 def test_streaming_and_chat(server):

@@ -43,6 +43,7 @@ class _Req:
     logprobs: Optional[list] = None       # per emitted token {token: logprob} (when requested)
     prompt_logprobs: Optional[list] = None
     stop_reason: Optional[object] = None
+    emits: int = 0                        # emit calls: the prefill's first token, then one per decode step
 
 
 class LLM:
@@ -610,15 +611,24 @@ class LLM:
         return [RequestOutput(r.rid, r.prompt, [CompletionOutput(
                     0, r.text if r.text is not None else self.tokenizer.decode(r.out), r.out, r.finish, r.stop_reason,
                     r.logprobs, (sum(d[t] for d, t in zip(r.logprobs, r.out)) if r.logprobs is not None else None))],
-                              metrics=dict(ttft_s=r.t_first - r.t_arrive, e2e_s=r.t_done - r.t_arrive),
+                              metrics=self._req_metrics(r),
                               prompt_logprobs=r.prompt_logprobs)
                 for r in reqs]
 
     # ------------------------------------------------------------------ helpers
+    @staticmethod
+    def _req_metrics(r: _Req) -> dict:
+        """Latencies and the request's acceptance length: tokens emitted per decode step after
+        the first token (1 + accepted drafts on average)."""
+        steps = max(r.emits - 1, 0)
+        return dict(ttft_s=r.t_first - r.t_arrive, e2e_s=r.t_done - r.t_arrive, decode_steps=steps,
+                    tokens_per_step=(len(r.out) - 1) / steps if steps else None)
+
     def _emit(self, r: _Req, tokens, logits=None) -> bool:
         """Append emitted tokens (stop conditions apply per token); `logits` [n, V] are the
         rows that predicted them (for requested logprobs)."""
         n0 = len(r.out)
+        r.emits += 1
         p = r.params
         entries = None
         if p.logprobs is not None and logits is not None:

@@ -294,6 +294,9 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
                        registry=registry, buckets=(0.001, 0.002, 0.005, 0.01, 0.02, 0.05, 0.1, 0.2, 0.5, 1))
     h_e2e = Histogram("moet_e2e_request_latency_seconds", "end-to-end request latency", registry=registry,
                       buckets=buckets)
+    h_acc = Histogram("moet_request_tokens_per_step", "tokens emitted per decode step of a request "
+                      "(1 + accepted draft tokens on average)", registry=registry,
+                      buckets=(1.0, 1.25, 1.5, 1.75, 2.0, 2.5, 3.0, 4.0, 5.0, 8.0))
 
     def run_request(prompt_ids, params):
         """-> (asyncio.Queue of (ids, finish, logprobs)) fed from the engine thread."""
@@ -307,8 +310,11 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
                 seen["first"] = now
                 h_ttft.observe(now - t0)
             seen["n"] += len(ids)
+            seen["calls"] = seen.get("calls", 0) + (1 if ids else 0)
             if finish is not None and not finish.startswith("error:"):
                 h_e2e.observe(now - t0)
+                if seen["calls"] > 1:        # one call per engine step after the first token
+                    h_acc.observe((seen["n"] - 1) / (seen["calls"] - 1))
                 if seen["first"] is not None and seen["n"] > 1:
                     h_tpot.observe((now - seen["first"]) / (seen["n"] - 1))
             loop.call_soon_threadsafe(aq.put_nowait, (list(ids), finish, lp))
