@@ -569,3 +569,34 @@ def test_gate_hidden_capture_shards(engine, tmp_path):
     steps = sum((g["steps"].tolist() for g in got), [])
     assert fired and steps == fired and len(shards) == (len(fired) + 1) // 2
     assert all(h.shape[1] == 4 for g in got for h in g["h"])
+
+
+def test_capped_gate_fire_step_w_ranks_by_routing_weight(engine):
+    """DELTA_RANK=step_w: a capped fire promotes the expert with this step's largest routing
+    weight first, whatever the decayed rank says."""
+    from vllm_moet_b200.residency import ConfidenceGate
+    from vllm_moet_b200.residency.delta import DeltaTier, delta_layout
+    llm = engine()
+    L, E, H, I = 2, 8, 64, 64
+    sb = delta_layout(H, I)[0]
+    llm.delta = DeltaTier([torch.zeros(E, sb, dtype=torch.uint8) for _ in range(L)], H, I, 16, device="cpu",
+                          policy="need")
+    llm.gate = ConfidenceGate(tau=2.0, fp_max=1, max_promote=1)
+    llm.delta_trace, llm.gate_log = None, None
+    llm.ecfg.moet.gate_fire_timing = False
+    llm.ecfg.moet.delta_rank = "step_w"
+    ids_of = lambda B: [torch.tensor([[int(t) % E, (int(t) + 1) % E] for t in    # noqa: E731
+                                      llm._states[B].tokens[:, 0].tolist()])] * L
+    llm.runner.route_ids = lambda B, st=None: ids_of(B)
+    # layer 0's second routed expert carries the heaviest weight; layer 1 the hottest rank
+    llm.runner.route_weights = lambda B: [torch.tensor([[0.1, 0.9]] * B), torch.tensor([[0.2, 0.3]] * B)]
+    llm.delta.freq[1, :] = 1000.0
+    calls = []
+    real = llm.delta.promote
+    llm.delta.promote = lambda pairs, **kw: (calls.append(list(pairs)), real(pairs, **kw))[1]
+    try:
+        llm.generate([[5, 6, 7]], SamplingParams(max_tokens=2, ignore_eos=True))
+    finally:
+        llm.delta.close()
+    (li, _), = calls[0]
+    assert li == 0                                          # the heaviest weight beats the hottest rank

@@ -210,6 +210,7 @@ class MoetConfig:
     delta_tick_ms: float = 50.0
     prefill_fp4: str = "1"              # "1": prefill serves delta-slot experts at FP4 too; "0": base only
     delta_decay: float = 0.98
+    delta_rank: str = "need"            # capped gate fires: "need" (decayed rank) | "step_w" (step's routing weight)
     promo_hyst: float = 0.0             # > 1: background promotions into a full pool need freq > h x victim + 4
     # base cache (GPU as expert cache)
     base_cache_gb: float = 0.0
@@ -290,6 +291,7 @@ class MoetConfig:
         "prefill_fp4": "VLLM_MOE_W2_PREFILL_FP4",
         "delta_decay": "VLLM_MOE_W2_DELTA_DECAY",
         "promo_hyst": "VLLM_MOE_W2_PROMO_HYST",
+        "delta_rank": "VLLM_MOE_W2_DELTA_RANK",
         "gate_spec_mask": "VLLM_MOE_W2_GATE_SPEC_MASK",
         "gate_trace": "VLLM_MOE_W2_GATE_TRACE",
         "gate_audit": "VLLM_MOE_W2_GATE_AUDIT",
@@ -355,6 +357,8 @@ class MoetConfig:
                 f"VLLM_MOE_W2_ZERO_MODE must be one of auto|sign|alt, got {self.zero_mode!r}")
         if self.delta_policy not in ("freq", "need", "lru"):
             raise ValueError(f"delta_policy must be freq|need|lru, got {self.delta_policy!r}")
+        if self.delta_rank not in ("need", "step_w"):
+            raise ValueError(f"VLLM_MOE_W2_DELTA_RANK must be need|step_w, got {self.delta_rank!r}")
         if self.replay_mode not in ("strict", "approximate"):
             raise ValueError(f"replay_mode must be strict|approximate, got {self.replay_mode!r}")
         if self.gate_signal not in ("maxprob", "margin"):

@@ -583,6 +583,17 @@ class NativeRunner:
             out.append(torch.cat(parts) if len(parts) > 1 else (parts[0] if parts else None))
         return out
 
+    def route_weights(self, B: int):
+        """The routing weights matching ``route_ids`` entry for entry."""
+        ws = self._bucket_ws(B)
+        out = []
+        for i in range(len(self._moe_index)):
+            parts = [ws.bufs.get((f"topk_w.{i}", torch.float32))]
+            parts += [ws.bufs.get((f"topk_w.{i}.p{j}", torch.float32)) for j in range(1, max(self.k, 1))]
+            parts = [t.reshape(-1) for t in parts if t is not None]
+            out.append(torch.cat(parts) if len(parts) > 1 else (parts[0] if parts else None))
+        return out
+
     def _ensure_experts(self, li, ids):
         """Eager passes (prefill, un-captured decode): fetch this layer's routed experts now."""
         if self.cache is None or li is None or torch.cuda.is_current_stream_capturing():
@@ -846,7 +857,8 @@ class NativeRunner:
         # per MoE layer (and per MTP draft pass: the MTP layer runs k times a step) its own
         # routing buffer, so the replay engine sees every expert the step routed to
         ids = self.ws.get("topk_ids" if mli is None else f"topk_ids.{mli}{self._route_tag}", (T, k), torch.int32)
-        wts = self.ws.get("topk_w", (T, k), torch.float32)
+        # routing weights per layer / draft pass too (the gate's step_w ranking reads them)
+        wts = self.ws.get("topk_w" if mli is None else f"topk_w.{mli}{self._route_tag}", (T, k), torch.float32)
         R = T * k
         ex = lw.experts
         L = ex.layout

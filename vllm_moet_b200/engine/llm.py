@@ -409,6 +409,21 @@ class LLM:
                 pairs += [(li, int(e)) for e in torch.unique(t).tolist()]
         return pairs
 
+    def _step_weights(self, B) -> dict:
+        """(layer, expert) -> the largest routing weight it got in the last decode step."""
+        out = {}
+        ws_fn = getattr(self.runner, "route_weights", None)
+        if ws_fn is None:
+            return out
+        for li, (ids, w) in enumerate(zip(self.runner.route_ids(B), ws_fn(B))):
+            if ids is None or w is None:
+                continue
+            for e, x in zip(ids.reshape(-1).tolist(), w.reshape(-1).tolist()):
+                k = (li, int(e))
+                if x > out.get(k, -1.0):
+                    out[k] = float(x)
+        return out
+
     def _routed_token_counts(self, B):
         """{(layer, expert): rows routed to it} of the last decode step."""
         out = {}
@@ -1234,7 +1249,11 @@ class LLM:
                     # a binding cap promotes the most-needed experts first (the tier's decayed
                     # rank: repeat offenders across fires), ties in routing order
                     fq = self.delta.freq
-                    promote = sorted(promote, key=lambda p: -float(fq[p[0], p[1]]))
+                    if m.delta_rank == "step_w":     # this step's heaviest routing weight first
+                        sw = self._step_weights(B)
+                        promote = sorted(promote, key=lambda p: (-sw.get(p, 0.0), -float(fq[p[0], p[1]])))
+                    else:
+                        promote = sorted(promote, key=lambda p: -float(fq[p[0], p[1]]))
                 promote = promote[: self.gate.max_promote]
                 t0 = time.perf_counter()
                 # fail-safe: a failed host read on any TP rank means no rank replays
