@@ -571,3 +571,34 @@ def test_delta_pool_sizing_from_gib_or_auto():
     assert delta_slots_for("auto", 1 << 20, 2 * G, reserve_gb=3.0) == 0
     with pytest.raises(ValueError):
         delta_slots_for("lots", 1 << 20, G)
+
+
+def test_prefill_fp4_ensure_makes_the_chunk_fp4_resident(monkeypatch):
+    """VLLM_MOE_W2_PREFILL_FP4=ensure: an eager prefill chunk makes its routed experts
+    resident in the delta tier before the layer's experts run (the most-routed ones when
+    the pool is smaller than the chunk's set); decode passes and mode 1 do not."""
+    import types
+    from vllm_moet_b200.config import MoetConfig
+    from vllm_moet_b200.engine.gpu_runner import NativeRunner
+    from vllm_moet_b200.residency.delta import DeltaTier, delta_layout
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: False)
+    H = I = 64
+    sb = delta_layout(H, I)[0]
+    delta = DeltaTier([torch.zeros(8, sb, dtype=torch.uint8) for _ in range(2)], H, I, 3, device="cpu",
+                      policy="need")
+    try:
+        fake = types.SimpleNamespace(cache=None, delta=delta,
+                                     ecfg=types.SimpleNamespace(moet=MoetConfig(prefill_fp4="ensure")))
+        ids = torch.tensor([[1, 2], [1, 5], [1, 2], [6, 2]])
+        NativeRunner._ensure_experts(fake, 0, ids, "decode")
+        assert not any(delta.resident(0, e) for e in range(8))
+        NativeRunner._ensure_experts(fake, 0, ids, "prefill")
+        assert delta.resident(0, 1) and delta.resident(0, 2)           # the two most routed
+        assert sum(delta.resident(0, e) for e in range(8)) == 3          # capped at the pool
+        fake.ecfg.moet = MoetConfig(prefill_fp4="1")
+        NativeRunner._ensure_experts(fake, 1, ids, "prefill")
+        assert not any(delta.resident(1, e) for e in range(8))
+    finally:
+        delta.close()
+    with pytest.raises(ValueError):
+        MoetConfig(prefill_fp4="sometimes").validate()

@@ -208,7 +208,8 @@ class MoetConfig:
     delta_policy: str = "freq"          # freq | need | lru
     delta_split: bool = False
     delta_tick_ms: float = 50.0
-    prefill_fp4: str = "1"              # "1": prefill serves delta-slot experts at FP4 too; "0": base only
+    prefill_fp4: str = "1"              # "1": prefill serves delta-slot experts at FP4 too; "0": base only;
+                                        # "ensure": each eager prefill chunk first makes its experts FP4-resident
     delta_decay: float = 0.98
     delta_rank: str = "need"            # capped gate fires: "need" (decayed rank) | "step_w" (step's routing weight)
     promo_hyst: float = 0.0             # > 1: background promotions into a full pool need freq > h x victim + 4
@@ -357,6 +358,8 @@ class MoetConfig:
                 f"VLLM_MOE_W2_ZERO_MODE must be one of auto|sign|alt, got {self.zero_mode!r}")
         if self.delta_policy not in ("freq", "need", "lru"):
             raise ValueError(f"delta_policy must be freq|need|lru, got {self.delta_policy!r}")
+        if str(self.prefill_fp4) not in ("0", "1", "ensure", ""):
+            raise ValueError(f"VLLM_MOE_W2_PREFILL_FP4 must be 0|1|ensure, got {self.prefill_fp4!r}")
         if self.delta_rank not in ("need", "step_w"):
             raise ValueError(f"VLLM_MOE_W2_DELTA_RANK must be need|step_w, got {self.delta_rank!r}")
         if self.replay_mode not in ("strict", "approximate"):

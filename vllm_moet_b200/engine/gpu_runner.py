@@ -594,11 +594,25 @@ class NativeRunner:
             out.append(torch.cat(parts) if len(parts) > 1 else (parts[0] if parts else None))
         return out
 
-    def _ensure_experts(self, li, ids):
-        """Eager passes (prefill, un-captured decode): fetch this layer's routed experts now."""
-        if self.cache is None or li is None or torch.cuda.is_current_stream_capturing():
+    def _ensure_experts(self, li, ids, mode: str = "decode"):
+        """Eager passes (prefill, un-captured decode): fetch this layer's routed experts now.
+        With VLLM_MOE_W2_PREFILL_FP4=ensure an eager prefill chunk also makes its routed
+        experts resident in the FP4 delta tier first, so every prefill pair is served at FP4
+        (the pool needs one layer's chunk working set; a larger set keeps the hottest)."""
+        if li is None or torch.cuda.is_current_stream_capturing():
             return
-        self.cache.ensure_resident(li, torch.unique(ids).tolist())
+        es = None
+        if self.cache is not None:
+            es = torch.unique(ids).tolist()
+            self.cache.ensure_resident(li, es)
+        if (self.delta is not None and mode in ("prefill", "cached")
+                and self.ecfg.moet.prefill_fp4 == "ensure"):
+            es = es if es is not None else torch.unique(ids).tolist()
+            cap = self.delta.n_slots
+            if len(es) > cap:               # keep the most-routed experts of the chunk
+                cnt = torch.bincount(ids.reshape(-1).long(), minlength=max(es) + 1)
+                es = sorted(es, key=lambda e: -int(cnt[e]))[:cap]
+            self.delta.ensure_resident(li, es)
 
     def set_pp_group(self, group):
         """Join a pipeline group: stage activations travel by NCCL send/recv and
@@ -906,7 +920,7 @@ class NativeRunner:
                               cfg.n_group, cfg.topk_group, cfg.norm_topk_prob, cfg.routed_scaling, ids, wts, MB,
                               rank, stok, posof, pairs, npairs, cnt, self.status, max(e_lo, 0), E_loc if ep else 0)
             self._looka_step(mli, hb, ids, ctx)
-            self._ensure_experts(mli, ids)
+            self._ensure_experts(mli, ids, ctx.mode)
             y2 = self._moe_gemv_pairs(h2q, h2s, stok, pairs, npairs, ex, R, MB, mli)
         else:
             # bf16 operands, fp32 accumulation; prefill-sized T runs on tensor-core tiles
@@ -919,7 +933,7 @@ class NativeRunner:
                 ids.copy_(pi)
                 wts.copy_(pw)
             self._looka_step(mli, hb, ids, ctx)
-            self._ensure_experts(mli, ids)
+            self._ensure_experts(mli, ids, ctx.mode)
             if tl is not None:      # trellis base tier: per-pair outputs, combined below
                 y2 = self.trellis.forward_pairs(tl, hb, ids, delta=self.trellis_delta)
                 posof = self.ws.get("trellis.nopos", (0,), torch.int32)
