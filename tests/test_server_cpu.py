@@ -406,3 +406,14 @@ def test_constrained_decoding_requests_are_refused(server):
     ok = requests.post(url + "/v1/completions", json={"prompt": [5, 6], "max_tokens": 2,
                                                       "response_format": {"type": "text"}}, timeout=120)
     assert ok.ok
+
+
+def test_chat_beam_search_over_http(server):
+    url, _ = server
+    r = requests.post(url + "/v1/chat/completions",
+                      json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 3, "n": 2,
+                            "use_beam_search": True, "ignore_eos": True}, timeout=300)
+    assert r.ok, r.text
+    ch = r.json()["choices"]
+    assert len(ch) == 2 and ch[0]["cumulative_logprob"] >= ch[1]["cumulative_logprob"]
+    assert all(c["message"]["role"] == "assistant" for c in ch)

@@ -427,17 +427,9 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
             return list(p)
         raise HTTPException(400, "prompt must be a string or a list of token ids")
 
-    async def beam_completion(body, params, plist, rid, created):
-        """``use_beam_search``: beam width = ``n`` (or ``best_of``), the search driven through
-        the engine queue -- each step's beams are one-token requests served concurrently."""
-        from ..engine.beam_search import BeamSearchParams, search_steps, step_params
-        if body.get("stream"):
-            raise HTTPException(400, "beam search does not stream")
-        try:
-            bp = BeamSearchParams(beam_width=int(body.get("best_of") or params.n), max_tokens=params.max_tokens,
-                                  ignore_eos=params.ignore_eos, length_penalty=float(body.get("length_penalty", 1.0)))
-        except ValueError as e:
-            raise HTTPException(400, str(e))
+    async def run_beams(plist, bp):
+        """The beam search over the engine queue: each step's beams are one-token requests."""
+        from ..engine.beam_search import search_steps, step_params
         gen = search_steps(plist, bp, tok.eos_token_id, tok.decode)
         sp = step_params(bp)
         try:
@@ -446,7 +438,24 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
                 res = await asyncio.gather(*[collect(run_request(b, sp)) for b in batch])
                 batch = gen.send([r[2][0] for r in res])
         except StopIteration as stop:
-            outs = stop.value
+            return stop.value
+
+    def beam_params(body, params):
+        from ..engine.beam_search import BeamSearchParams
+        if body.get("stream"):
+            raise HTTPException(400, "beam search does not stream")
+        try:
+            return BeamSearchParams(beam_width=int(body.get("best_of") or params.n), max_tokens=params.max_tokens,
+                                    ignore_eos=params.ignore_eos,
+                                    length_penalty=float(body.get("length_penalty", 1.0)))
+        except ValueError as e:
+            raise HTTPException(400, str(e))
+
+    async def beam_completion(body, params, plist, rid, created):
+        """``use_beam_search``: beam width = ``n`` (or ``best_of``), the search driven through
+        the engine queue -- each step's beams are one-token requests served concurrently."""
+        bp = beam_params(body, params)
+        outs = await run_beams(plist, bp)
         choices, n_out = [], 0
         for j, o in enumerate(outs):
             for s_ in o.sequences[:params.n]:
@@ -537,6 +546,16 @@ def build_app(worker: EngineWorker, reasoning_parser: Optional[str] = "deepseek_
         prompt = [tok.bos_token_id] + tok.encode(text)
         rid, created = f"chatcmpl-{uuid.uuid4().hex[:24]}", int(time.time())
         thinking = chat_encoding.normalize_effort(effort) is not None
+        if body.get("use_beam_search"):       # beam search: n best beams as n choices
+            outs = await run_beams([prompt], beam_params(body, params))
+            seqs = outs[0].sequences[:params.n]
+            n_out = sum(len(q.generated) for q in seqs)
+            return JSONResponse({"id": rid, "object": "chat.completion", "created": created, "model": name,
+                                 "choices": [{"index": i, "message": {"role": "assistant", "content": q.text},
+                                              "finish_reason": q.finish_reason,
+                                              "cumulative_logprob": q.cum_logprob} for i, q in enumerate(seqs)],
+                                 "usage": {"prompt_tokens": len(prompt), "completion_tokens": n_out,
+                                           "total_tokens": len(prompt) + n_out}})
         if body.get("stream") and params.n != 1:
             raise HTTPException(400, "streaming serves one completion per request")
         qs = [run_request(prompt, c) for c in copies(params)]
