@@ -194,6 +194,8 @@ def test_cli_flags_map_to_engine_arguments():
                                                "--enable-chunked-prefill", "--max-num-batched-tokens", "512"]))
     assert kw["enable_prefix_caching"] and kw["prefix_block_size"] == 32
     assert kw["enable_chunked_prefill"] and kw["max_num_batched_tokens"] == 512
+    assert "trellis_pack" not in kw
+    assert llm_kwargs(build_parser().parse_args(["--trellis-pack", "/packs"]))["trellis_pack"] == "/packs"
     from vllm_moet_b200.entrypoints.openai_server import _params_from
     sp = _params_from({"presence_penalty": 0.5, "frequency_penalty": 0.25, "repetition_penalty": 1.1,
                        "min_p": 0.05, "logit_bias": {"42": -100}})

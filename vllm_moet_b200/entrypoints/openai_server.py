@@ -647,6 +647,8 @@ def build_parser():
                     "from the free memory after the weights")
     ap.add_argument("--trust-remote-code", action="store_true", help="accepted; no remote code is run")
     ap.add_argument("--dtype", default="auto", help="accepted; activations are bf16")
+    ap.add_argument("--trellis-pack", default=None,
+                    help="serve the routed experts from these trellis (EXL3-style) packs (one rank)")
     return ap
 
 
@@ -676,7 +678,8 @@ def llm_kwargs(args, world: int = 1, rank: int = 0, group=None) -> dict:
                 enable_prefix_caching=bool(getattr(args, "enable_prefix_caching", False)),
                 prefix_block_size=int(getattr(args, "block_size", 16)),
                 enable_chunked_prefill=bool(getattr(args, "enable_chunked_prefill", False)),
-                max_num_batched_tokens=getattr(args, "max_num_batched_tokens", None))
+                max_num_batched_tokens=getattr(args, "max_num_batched_tokens", None),
+                **({"trellis_pack": args.trellis_pack} if getattr(args, "trellis_pack", None) else {}))
 
 
 def main(argv=None):
