@@ -667,7 +667,7 @@ def llm_kwargs(args, world: int = 1, rank: int = 0, group=None) -> dict:
     if args.pipeline_parallel_size != 1:
         raise SystemExit("--pipeline-parallel-size: the server runs TP ranks; use the LLM API for pipeline stages")
     if args.decode_context_parallel_size != 1:
-        raise SystemExit("--decode-context-parallel-size: DCP runs on the CPU engine only so far")
+        raise SystemExit("--decode-context-parallel-size: the server runs TP ranks; use the LLM API with dcp_group")
     kv = "nvfp4" if args.kv_cache_dtype == "nvfp4" else "bf16"
     return dict(device=args.device, num_speculative_tokens=0 if method in ("dspark", "dflash") else k,
                 max_model_len=args.max_model_len,
