@@ -369,3 +369,22 @@ def test_request_acceptance_metrics(tiny_llm):
     m = o.metrics
     assert m["decode_steps"] >= 1 and 1.0 <= m["tokens_per_step"] <= tiny_llm.k + 1
     assert abs(m["tokens_per_step"] * m["decode_steps"] - (len(o.outputs[0].token_ids) - 1)) < 1e-9
+
+
+def test_bad_words(tiny_llm):
+    """bad_words / bad_word_ids (vLLM's fields): a one-token word never appears; a
+    two-token word's second token is banned only right after its first."""
+    p = [5, 9, 17, 33]
+    sp = SamplingParams(max_tokens=6, ignore_eos=True)
+    g = tiny_llm.generate([p], sp)[0].outputs[0].token_ids
+    one = tiny_llm.generate([p], SamplingParams(max_tokens=6, ignore_eos=True, bad_word_ids=[[g[1]]]))
+    one = one[0].outputs[0].token_ids
+    assert g[1] not in one and one[0] == g[0]
+    two = tiny_llm.generate([p], SamplingParams(max_tokens=6, ignore_eos=True, bad_word_ids=[[g[0], g[1]]]))
+    two = two[0].outputs[0].token_ids
+    assert two[0] == g[0] and two[1] != g[1]
+    assert all(not (a == g[0] and b == g[1]) for a, b in zip(two, two[1:]))
+    # words are tokenized by the engine (the word and its leading-space form)
+    sw = SamplingParams(max_tokens=2, ignore_eos=True, bad_words=["ab"])
+    tiny_llm.generate([p], sw)
+    assert sw.bad_word_ids and all(isinstance(t, int) for w in sw.bad_word_ids for t in w)

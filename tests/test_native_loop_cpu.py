@@ -600,3 +600,12 @@ def test_capped_gate_fire_step_w_ranks_by_routing_weight(engine):
         llm.delta.close()
     (li, _), = calls[0]
     assert li == 0                                          # the heaviest weight beats the hottest rank
+
+
+def test_one_token_bad_words_in_the_gpu_loop(engine):
+    """One-token bad words on the GPU loop: the row's dense bias bans them."""
+    llm = engine()
+    want = chain([5, 6, 7], 6)
+    out = llm.generate([[5, 6, 7]], SamplingParams(max_tokens=6, ignore_eos=True, bad_word_ids=[[want[2]]]))
+    got = out[0].outputs[0].token_ids
+    assert want[2] not in got and got[:2] == want[:2]

@@ -1676,6 +1676,10 @@ class DecodeState:
         if params.allowed_token_ids is not None:     # only these tokens: the rest biased out
             from ..spec.logits_process import allowed_bias
             pr["bias"][row] += allowed_bias(params.allowed_token_ids, V, dev)
+        one = [w[0] for w in (params.bad_word_ids or []) if len(w) == 1 and 0 <= w[0] < V]
+        if one:                                      # one-token bad words: always banned
+            from ..spec.logits_process import DISALLOWED
+            pr["bias"][row, torch.tensor(one, dtype=torch.long).to(dev)] += DISALLOWED
 
     def count_tokens(self, rows, tokens):
         """Generated tokens of the last step (host lists) into the rows' counts."""

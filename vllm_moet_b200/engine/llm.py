@@ -568,6 +568,16 @@ class LLM:
         return self.generate(prompts, sampling_params)
 
     def _check_request(self, t, sp):
+        if sp.bad_words and sp.bad_word_ids is None:     # vLLM: the word and its leading-space form
+            ids = []
+            for w in sp.bad_words:
+                for form in (w, " " + w.lstrip()):
+                    seq = list(self.tokenizer.encode(form))
+                    if seq and seq not in ids:
+                        ids.append(seq)
+            sp.bad_word_ids = ids
+        if sp.bad_word_ids and self.device.type == "cuda" and any(len(w) > 1 for w in sp.bad_word_ids):
+            raise NotImplementedError("bad_words of several tokens: CPU engine (the GPU bans one-token words)")
         if sp.prompt_logprobs is not None and self.device.type == "cuda":
             raise NotImplementedError("prompt_logprobs: the GPU prefill keeps only each prompt's last logits")
         if sp.processes_logits or sp.min_p > 0:

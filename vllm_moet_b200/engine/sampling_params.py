@@ -27,6 +27,8 @@ class SamplingParams:
     logit_bias: Optional[Dict[int, float]] = None   # token id -> added to its logit
     min_p: float = 0.0              # sampling: drop tokens below min_p x the top token's probability
     allowed_token_ids: Optional[List[int]] = None   # only these tokens can be chosen (vLLM's field)
+    bad_words: Optional[List[str]] = None           # never generate these words (vLLM's field)
+    bad_word_ids: Optional[List[List[int]]] = None  # the same as token sequences (filled from bad_words)
 
     def __post_init__(self):
         if isinstance(self.stop, str):
@@ -50,6 +52,10 @@ class SamplingParams:
             raise ValueError("presence_penalty and frequency_penalty must be in [-2, 2]")
         if self.logit_bias:
             self.logit_bias = {int(k): float(v) for k, v in self.logit_bias.items()}
+        if isinstance(self.bad_words, str):
+            self.bad_words = [self.bad_words]
+        if self.bad_word_ids is not None:
+            self.bad_word_ids = [[int(t) for t in w] for w in self.bad_word_ids if len(w)]
         if self.allowed_token_ids is not None:
             self.allowed_token_ids = sorted({int(t) for t in self.allowed_token_ids})
             if not self.allowed_token_ids:
@@ -59,7 +65,8 @@ class SamplingParams:
     def processes_logits(self) -> bool:
         """Whether the logits are changed before choosing a token (penalties, bias)."""
         return bool(self.presence_penalty or self.frequency_penalty or self.repetition_penalty != 1.0
-                    or self.logit_bias or self.allowed_token_ids is not None)
+                    or self.logit_bias or self.allowed_token_ids is not None or bool(self.bad_words)
+                    or bool(self.bad_word_ids))
 
 
 def find_stop(text: str, stops: List[str], start: int = 0):

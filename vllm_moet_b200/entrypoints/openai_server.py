@@ -191,7 +191,7 @@ def _params_from(body: Dict[str, Any], default_max: int = 16) -> SamplingParams:
                           repetition_penalty=float(body.get("repetition_penalty") or 1.0),
                           min_p=float(body.get("min_p") or 0.0),
                           logit_bias={int(k): float(v) for k, v in (body.get("logit_bias") or {}).items()} or None,
-                          allowed_token_ids=body.get("allowed_token_ids"))
+                          allowed_token_ids=body.get("allowed_token_ids"), bad_words=body.get("bad_words"))
 
 
 class _ChatParseStream:

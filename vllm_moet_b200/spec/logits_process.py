@@ -54,4 +54,13 @@ def process_logits(logits: torch.Tensor, sp, prompt: Sequence[int], out: Sequenc
             x[:, ids] += torch.tensor([sp.logit_bias[int(t)] for t in ids], device=dev)
     if sp.allowed_token_ids is not None:
         x = x + allowed_bias(sp.allowed_token_ids, V, dev)[None]
+    for w in sp.bad_word_ids or []:
+        # a bad word's last token is banned on the rows whose history ends with the word's
+        # other tokens (a one-token word: always)
+        if not 0 <= w[-1] < V:
+            continue
+        for j in range(R):
+            hist = list(out) + [int(d) for d in drafts[:j]]
+            if len(w) == 1 or (len(hist) >= len(w) - 1 and hist[len(hist) - len(w) + 1:] == w[:-1]):
+                x[j, w[-1]] += DISALLOWED
     return x
