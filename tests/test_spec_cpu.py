@@ -89,6 +89,11 @@ def test_quant_study_orders_formats():
     from vllm_moet_b200.tools.quant_study import study
     r = study(torch.randn(64, 256) * 0.02)
     assert r["nvfp4"][0] < r["2-bit codebook (auto)"][0] and r["mxfp4 (delta tier)"][0] < r["2-bit codebook (auto)"][0]
+    t = study(torch.randn(64, 256) * 0.02, trellis_L=8)
+    # the trellis at 2 bits beats the 2-bit codebook at about the same bits, 3 bits beats both
+    assert t["trellis 2-bit (L=8)"][0] < t["2-bit codebook (auto)"][0] < 1.0
+    assert t["trellis 3-bit (L=8)"][0] < t["trellis 2-bit (L=8)"][0]
+    assert 2.0 < t["trellis 2-bit (L=8)"][1] < 2.5
 
 
 def test_filter_probs_top_k_top_p():

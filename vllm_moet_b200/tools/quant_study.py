@@ -5,7 +5,8 @@
 Compares, on the same random (or heavy-tailed) matrix: NVFP4 (e2m1, e4m3
 block-16 scales), MXFP4 (e2m1, UE8M0 block-32: the FP4 delta tier), and the
 sign-symmetric 2-bit codebook derived from NVFP4 with each zero-code mode
-(the base tier).  Prints relative Frobenius error and bits per weight
+(the base tier) and, with ``--trellis-L``, the trellis (EXL3-style) base tier at 2 and 3
+bits (its bits per weight include the fp16 row / column vectors).  Prints relative Frobenius error and bits per weight
 (reference: the offline codebook studies, tools/sweep_nvfp4_codebook.py).
 """
 from __future__ import annotations
@@ -17,7 +18,7 @@ import torch
 from ..formats import codebook, planes
 
 
-def study(w: torch.Tensor) -> dict:
+def study(w: torch.Tensor, trellis_L: int = 0) -> dict:
     N, K = w.shape
     res = {}
     ts = float(w.abs().max()) / (6.0 * 448.0)
@@ -32,6 +33,13 @@ def study(w: torch.Tensor) -> dict:
         codes, s, _ = codebook.nvfp4_to_codes_scales(packed, sf, t2, mode=mode)
         d = codebook.dequant_codes(codes, s)
         res[f"2-bit codebook ({mode})"] = (float((d - w).norm() / w.norm()), 2.25)
+    if trellis_L:
+        from ..formats import trellis
+        for bits in (2, 3):
+            t = trellis.quantize_linear(w, bits, trellis_L)
+            d = trellis.dequant_linear(t, bits, trellis_L)
+            res[f"trellis {bits}-bit (L={trellis_L})"] = (float((d - w).norm() / w.norm()),
+                                                        8.0 * trellis.linear_bytes(N, K, bits) / (N * K))
     return res
 
 
@@ -42,13 +50,14 @@ def main(argv=None):
     ap.add_argument("--std", type=float, default=0.02)
     ap.add_argument("--heavy-tail", action="store_true", help="Student-t (3 dof) weights")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--trellis-L", type=int, default=0, help="also the trellis tier with 2^L states (0: off)")
     a = ap.parse_args(argv)
     g = torch.Generator().manual_seed(a.seed)
     if a.heavy_tail:
         w = torch.distributions.StudentT(3.0).sample((a.rows, a.cols)) * a.std
     else:
         w = torch.randn(a.rows, a.cols, generator=g) * a.std
-    for name, (err, bits) in study(w).items():
+    for name, (err, bits) in study(w, a.trellis_L).items():
         print(f"{name:28s} rel err {err:.4f}   {bits:.2f} bits/weight")
 
 
