@@ -363,6 +363,9 @@ class LLM:
         release stores and peer buffers."""
         if hasattr(self, "_decode_steps"):
             self.dump_traces()
+        kpi = getattr(self, "kpi", None)
+        if kpi is not None and kpi.steps % kpi.every:      # the last partial window's KPI line
+            kpi.flush()
         self._dump_heat()
         if getattr(self, "gate_log", None) is not None:
             self.gate_log.close()
